@@ -1,0 +1,460 @@
+"""CPU oracle for the sa3.cpp adapter-training hot path.
+
+TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline /
+reference legs import this module, and only as the checker; the product path (the sa3k CUDA
+library and its host API) never calls it.
+
+It restates, in float64 numpy (and float64 torch autograd where a whole block is differentiated),
+the reference's math for the path:
+
+  quant formats      oracle/quant.c (C), pinned against gguf-py golden vectors
+  dit_lin            src/dit.h:92-149        functional LoRA / DoRA-rows linear, forward
+  dit_lin backward   what ggml_build_backward_expand (src/train_ckpt.h:400) derives for the ops
+                     of src/dit.h:106-147, written out by hand (pinned by finite differences,
+                     as tests/dit_lin_functional_test.cpp:132-260 does)
+  W_eff              src/train_lora.h:301-329 (materialized effective weight, dora-rows)
+  row norms          src/train_lora.h:141-174
+  rms_norm           src/nn.h:40-42
+  rope_neox          src/nn.h:53-59 (partial NeoX rotation of the first n_dims of each head)
+  sdpa               src/nn.h:135-144 (+ the band mask |q-k| <= window of src/same_ae.h:96-106)
+  dit_diff_attn      src/dit.h:152-158
+  dit_block          src/dit.h:164-266 (autodiff_safe form, no local-cond)
+  dit_head/tail      src/dit.h:286-323
+  loss               src/train_ckpt.h:226-228 (mean squared error over io*frames)
+  average + clip     src/train_loop.h:147-171
+  AdamW              src/train_optimizer.h:42-65 (the reference's own compiled code is
+                     oracle/_ref/libsa3ref.so; adamw_f32 below restates it)
+  expo_features      src/sa3_pipeline.h:57-67
+
+Layout convention: ggml [ne0, ne1] is row-major [ne1][ne0].  So W [in,out] is W[out][in]
+(quant blocks run along `in`), x [in,S] is x[S][in], A [in,r] is A[r][in], B [r,out] is B[out][r].
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+QK8_0, Q8_0_BYTES = 32, 34
+QK_K, Q4_K_BYTES = 256, 144
+
+
+# --------------------------------------------------------------------------------------------
+# C restatement (oracle/quant.c) and the reference's own compiled headers (oracle/_ref)
+# --------------------------------------------------------------------------------------------
+def _load(path):
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} missing: run `make -C oracle` (or __graft_entry__.build())")
+    return ctypes.CDLL(path)
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        _lib = _load(os.path.join(_HERE, "liboracle.so"))
+        P, I64 = ctypes.c_void_p, ctypes.c_int64
+        for name in ("oracle_quantize_q8_0", "oracle_dequantize_q8_0", "oracle_quantize_q4_k",
+                     "oracle_dequantize_q4_k"):
+            getattr(_lib, name).argtypes = [P, P, I64]
+            getattr(_lib, name).restype = None
+        _lib.oracle_row_norm_sq.argtypes = [P, I64, I64, ctypes.c_float, P, P]
+        _lib.oracle_row_norm_sq.restype = None
+    return _lib
+
+
+def ref_available():
+    return os.path.exists(os.path.join(_HERE, "_ref", "libsa3ref.so"))
+
+
+def ref():
+    """The reference's own train_optimizer.h / train_diffusion.h, compiled by oracle/Makefile."""
+    global _ref
+    if _ref is None:
+        _ref = _load(os.path.join(_HERE, "_ref", "libsa3ref.so"))
+        P, F, I = ctypes.c_void_p, ctypes.c_float, ctypes.c_int
+        _ref.sa3ref_adamw_update.argtypes = [P, P, P, P, ctypes.c_long, F, F, F, F, F, I,
+                                             ctypes.c_char_p, I]
+        _ref.sa3ref_adamw_update.restype = I
+        _ref.sa3ref_inverse_lr.argtypes = [F, I, F, F, F, F]
+        _ref.sa3ref_inverse_lr.restype = F
+        _ref.sa3ref_diffusion_sample_at.argtypes = [ctypes.c_ulonglong, P, ctypes.c_long, F, P, P, P]
+        _ref.sa3ref_diffusion_sample_at.restype = I
+    return _ref
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def quantize(w: np.ndarray, qtype: str) -> np.ndarray:
+    """Row-wise quantize W[out][in] (blocks along `in`) into raw GGUF bytes [out][row_bytes]."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out, inn = w.shape
+    if qtype == "q8_0":
+        assert inn % QK8_0 == 0
+        raw = np.empty((out, inn // QK8_0 * Q8_0_BYTES), np.uint8)
+        lib().oracle_quantize_q8_0(_ptr(w), _ptr(raw), w.size)
+    elif qtype == "q4_k":
+        assert inn % QK_K == 0
+        raw = np.empty((out, inn // QK_K * Q4_K_BYTES), np.uint8)
+        lib().oracle_quantize_q4_k(_ptr(w), _ptr(raw), w.size)
+    elif qtype == "f16":
+        raw = np.ascontiguousarray(w.astype(np.float16)).view(np.uint8).reshape(out, inn * 2)
+    elif qtype == "f32":
+        raw = w.view(np.uint8).reshape(out, inn * 4).copy()
+    else:
+        raise ValueError(qtype)
+    return raw
+
+
+def dequantize(raw: np.ndarray, qtype: str, out: int, inn: int) -> np.ndarray:
+    raw = np.ascontiguousarray(raw, dtype=np.uint8)
+    y = np.empty((out, inn), np.float32)
+    if qtype == "q8_0":
+        lib().oracle_dequantize_q8_0(_ptr(raw), _ptr(y), y.size)
+    elif qtype == "q4_k":
+        lib().oracle_dequantize_q4_k(_ptr(raw), _ptr(y), y.size)
+    elif qtype == "f16":
+        y[...] = raw.view(np.float16).reshape(out, inn).astype(np.float32)
+    elif qtype == "f32":
+        y[...] = raw.view(np.float32).reshape(out, inn)
+    else:
+        raise ValueError(qtype)
+    return y
+
+
+def row_norms(w: np.ndarray, eps: float = 1e-12):
+    """(base_norm_sq, norm) per output row, f64 accumulation: src/train_lora.h:141-174."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    out, inn = w.shape
+    nsq = np.empty(out, np.float32)
+    nrm = np.empty(out, np.float32)
+    lib().oracle_row_norm_sq(_ptr(w), inn, out, ctypes.c_float(eps), _ptr(nsq), _ptr(nrm))
+    return nsq, nrm
+
+
+# --------------------------------------------------------------------------------------------
+# dit_lin: functional LoRA / DoRA-rows linear (src/dit.h:92-149), forward and backward
+# --------------------------------------------------------------------------------------------
+def dit_lin_fwd(x, W, A=None, B=None, scale=1.0, m=None, bns=None, bias=None):
+    """y[S][out].  x[S][in], W[out][in], A[r][in], B[out][r], m/bns[out].  float64.
+
+    y = g * (x W^T + s (x A^T) B^T) + bias,  g = m / sqrt(bns + 2s t2 + s^2 t3)  (dora)
+    t2[o] = sum_r (W A^T)[o,r] B[o,r]          (src/dit.h:132-135)
+    t3[o] = sum_r B[o,r] (B A A^T)[o,r]         (src/dit.h:136-138)
+    """
+    x = np.asarray(x, np.float64)
+    W = np.asarray(W, np.float64)
+    z = x @ W.T
+    cache = {"x": x, "W": W}
+    if A is not None:
+        A = np.asarray(A, np.float64)
+        B = np.asarray(B, np.float64)
+        u = x @ A.T
+        z = z + scale * (u @ B.T)
+        cache.update(A=A, B=B, u=u, scale=scale)
+        if m is not None:
+            m = np.asarray(m, np.float64)
+            bns = np.asarray(bns, np.float64)
+            P = W @ A.T
+            AAt = A @ A.T
+            BAAt = B @ AAt
+            t2 = (P * B).sum(1)
+            t3 = (BAAt * B).sum(1)
+            nsq = bns + 2.0 * scale * t2 + scale * scale * t3
+            g = m / np.sqrt(nsq)
+            cache.update(m=m, P=P, BAAt=BAAt, nsq=nsq, g=g, z=z)
+            y = z * g
+        else:
+            y = z
+    else:
+        y = z
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    return y, cache
+
+
+def dit_lin_bwd(dy, cache):
+    """Gradients of dit_lin for upstream dy[S][out]: dict(dx, dA, dB, dm)."""
+    dy = np.asarray(dy, np.float64)
+    x, W = cache["x"], cache["W"]
+    out = {}
+    if "g" in cache:
+        g, z, m, nsq = cache["g"], cache["z"], cache["m"], cache["nsq"]
+        dz = dy * g
+        dg = (dy * z).sum(0)
+        out["dm"] = dg / np.sqrt(nsq)
+        dnsq = -0.5 * dg * g / nsq
+    else:
+        dz = dy
+        dnsq = None
+    dx = dz @ W
+    if "A" in cache:
+        A, B, u, s = cache["A"], cache["B"], cache["u"], cache["scale"]
+        dB = s * dz.T @ u
+        du = s * dz @ B
+        dA = du.T @ x
+        dx = dx + du @ A
+        if dnsq is not None:
+            P, BAAt = cache["P"], cache["BAAt"]
+            dt2 = 2.0 * s * dnsq
+            dt3 = s * s * dnsq
+            # t2 = sum_r P B:  dB += dt2 P ; dP = dt2 B ; dA += dP^T W
+            dB = dB + dt2[:, None] * P
+            dA = dA + (dt2[:, None] * B).T @ W
+            # t3 = |B A|_row^2:  dB += 2 dt3 (B A A^T) ; dA += 2 (B^T diag(dt3) B) A
+            dB = dB + 2.0 * dt3[:, None] * BAAt
+            dA = dA + 2.0 * (B.T @ (dt3[:, None] * B)) @ A
+        out["dA"] = dA
+        out["dB"] = dB
+    out["dx"] = dx
+    return out
+
+
+def effective_weight(W, A, B, scale, m=None):
+    """Materialized W_eff[out][in] (src/train_lora.h:301-329): lora or dora-rows."""
+    W = np.asarray(W, np.float64)
+    v = W + scale * (np.asarray(B, np.float64) @ np.asarray(A, np.float64))
+    if m is None:
+        return v
+    inn = W.shape[1]
+    # rms_norm(v, 1e-12) / sqrt(in) == v / sqrt(sum v^2 + in*1e-12)
+    nrm = np.sqrt((v * v).sum(1) + inn * 1e-12)
+    return v / nrm[:, None] * np.asarray(m, np.float64)[:, None]
+
+
+# --------------------------------------------------------------------------------------------
+# attention pieces (float64 torch so the whole block can be differentiated by autograd)
+# --------------------------------------------------------------------------------------------
+def _torch():
+    import torch
+    return torch
+
+
+def rms_norm(x, gamma, eps):
+    """src/nn.h:40-42: x / sqrt(mean(x^2) + eps) * gamma over the last dim."""
+    torch = _torch()
+    return x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps) * gamma
+
+
+def rope_neox(x, pos, n_dims, base):
+    """src/nn.h:53-59 (ggml_rope_ext, NEOX, freq_scale 1, no extrapolation): x[..., S, H, D]
+    with pos[S]; pairs (i, i + n_dims/2) for i < n_dims/2 rotate by pos * base^(-2i/n_dims);
+    dims >= n_dims pass through."""
+    torch = _torch()
+    half = n_dims // 2
+    i = torch.arange(half, dtype=torch.float64)
+    theta = pos.to(torch.float64)[:, None] * torch.pow(torch.tensor(base, dtype=torch.float64), -2.0 * i / n_dims)
+    c = torch.cos(theta)[:, None, :]
+    s = torch.sin(theta)[:, None, :]
+    x0, x1, rest = x[..., :half], x[..., half:n_dims], x[..., n_dims:]
+    return torch.cat([x0 * c - x1 * s, x0 * s + x1 * c, rest], -1)
+
+
+def sdpa(q, k, v, scale, window=None):
+    """src/nn.h:135-144: softmax(scale q k^T) v per head.  q[H,Sq,D], k/v[H,Sk,D].
+    window: None = dense (the DiT); w = keep |i - j| <= w (the band of src/same_ae.h:96-106)."""
+    torch = _torch()
+    s = torch.matmul(q, k.transpose(-1, -2)) * scale
+    if window is not None:
+        iq = torch.arange(q.shape[-2])[:, None]
+        ik = torch.arange(k.shape[-2])[None, :]
+        s = s.masked_fill((iq - ik).abs() > window, float("-inf"))
+    p = torch.softmax(s, -1)
+    return torch.matmul(p, v)
+
+
+def silu(x):
+    torch = _torch()
+    return x * torch.sigmoid(x)
+
+
+# --------------------------------------------------------------------------------------------
+# the DiT (src/dit.h) in float64 torch; weights are dequantized float tensors
+# --------------------------------------------------------------------------------------------
+class DitCfg:
+    def __init__(self, io=64, dim=1536, depth=24, heads=24, head_dim=64, cond_dim=768,
+                 mem_tokens=64, rot=32, time_dim=256, ff_inner=6144, differential=False,
+                 rope_base=10000.0, norm_eps=1e-5, qk_eps=1e-6, time_min_freq=0.5,
+                 time_max_freq=10000.0):
+        self.io, self.dim, self.depth, self.heads, self.head_dim = io, dim, depth, heads, head_dim
+        self.cond_dim, self.mem_tokens, self.rot, self.time_dim = cond_dim, mem_tokens, rot, time_dim
+        self.ff_inner, self.differential, self.rope_base = ff_inner, differential, rope_base
+        self.norm_eps, self.qk_eps = norm_eps, qk_eps
+        self.time_min_freq, self.time_max_freq = time_min_freq, time_max_freq
+
+    @property
+    def qkv_mult(self):
+        return 5 if self.differential else 3
+
+
+def expo_features(t, dim, min_f, max_f):
+    """src/sa3_pipeline.h:57-67 ([cos, sin] of t * f * 2pi, f log-spaced), float32 like the host."""
+    half = dim // 2
+    lmin, lmax = np.float32(math.log(min_f)), np.float32(math.log(max_f))
+    out = np.empty(dim, np.float32)
+    for i in range(half):
+        ramp = np.float32(i / (half - 1)) if half > 1 else np.float32(0)
+        freq = np.float32(np.exp(np.float32(ramp * (lmax - lmin) + lmin)))
+        arg = np.float32(np.float32(t) * freq * np.float32(6.28318530717958648))
+        out[i] = np.cos(arg)
+        out[half + i] = np.sin(arg)
+    return out
+
+
+def lin(Wd, lora, name, x, bias=None):
+    """dit_lin over torch tensors: Wd[name] is W[out][in]; lora[name] = dict(A,B,m,bns,scale)."""
+    torch = _torch()
+    W = Wd[name]
+    y = torch.matmul(x, W.t())
+    p = lora.get(name) if lora else None
+    if p is not None:
+        A, B, s = p["A"], p["B"], p["scale"]
+        y = y + s * torch.matmul(torch.matmul(x, A.t()), B.t())
+        if p.get("m") is not None:
+            P = torch.matmul(W, A.t())
+            t2 = (P * B).sum(1)
+            t3 = (torch.matmul(B, torch.matmul(A, A.t())) * B).sum(1)
+            nsq = p["bns"] + 2.0 * s * t2 + s * s * t3
+            y = y * (p["m"] / torch.sqrt(nsq))
+    if bias is not None:
+        y = y + bias
+    return y
+
+
+def dit_block(Wd, lora, pfx, x, context, gcond, pos, c: DitCfg, window=None):
+    """src/dit.h:164-266 for one sample: x[S][dim], context[Ctx][dim], gcond[6*dim]."""
+    torch = _torch()
+    dim, hd, nh = c.dim, c.head_dim, c.heads
+    S, Ctx = x.shape[0], context.shape[0]
+    scale = 1.0 / math.sqrt(hd)
+    ssg = Wd[pfx + "ssg"] + gcond
+    sc_a, sh_a, g_a, sc_f, sh_f, g_f = [ssg[i * dim:(i + 1) * dim] for i in range(6)]
+
+    def heads(a, n):
+        return a.reshape(n, nh, hd)
+
+    def to_attn(a):  # [n, H, D] -> [H, n, D]
+        return a.permute(1, 0, 2)
+
+    def attn(qa, ka, va, win):
+        o = sdpa(to_attn(qa), to_attn(ka), to_attn(va), scale, win)   # [H, Sq, D]
+        return o.permute(1, 0, 2).reshape(-1, dim)
+
+    gate = lambda h, g: h / (torch.exp(g - 1.0) + 1.0)   # h * sigmoid(1 - g), src/dit.h:186-193
+    res = x
+    h = rms_norm(x, Wd[pfx + "pre_norm.gamma"], c.norm_eps) * (1.0 + sc_a) + sh_a
+    qkv = lin(Wd, lora, pfx + "self.qkv.weight", h)
+    sl = lambda t, i: t[:, i * dim:(i + 1) * dim]
+    q = rms_norm(heads(sl(qkv, 0), S), Wd[pfx + "self.q_norm.gamma"], c.qk_eps)
+    k = rms_norm(heads(sl(qkv, 1), S), Wd[pfx + "self.k_norm.gamma"], c.qk_eps)
+    v = heads(sl(qkv, 2), S)
+    q = rope_neox(q, pos, c.rot, c.rope_base)
+    k = rope_neox(k, pos, c.rot, c.rope_base)
+    o = attn(q, k, v, window)
+    if c.differential:
+        qd = rope_neox(rms_norm(heads(sl(qkv, 3), S), Wd[pfx + "self.q_norm.gamma"], c.qk_eps), pos, c.rot, c.rope_base)
+        kd = rope_neox(rms_norm(heads(sl(qkv, 4), S), Wd[pfx + "self.k_norm.gamma"], c.qk_eps), pos, c.rot, c.rope_base)
+        o = o - attn(qd, kd, v, window)
+    o = lin(Wd, lora, pfx + "self.out.weight", o)
+    x = res + gate(o, g_a)
+
+    hc = rms_norm(x, Wd[pfx + "cross_norm.gamma"], c.norm_eps)
+    qf = lin(Wd, lora, pfx + "cross.q.weight", hc)
+    kv = lin(Wd, lora, pfx + "cross.kv.weight", context)
+    cq = rms_norm(heads(sl(qf, 0), S), Wd[pfx + "cross.q_norm.gamma"], c.qk_eps)
+    ck = rms_norm(heads(sl(kv, 0), Ctx), Wd[pfx + "cross.k_norm.gamma"], c.qk_eps)
+    if c.differential:
+        cqd = rms_norm(heads(sl(qf, 1), S), Wd[pfx + "cross.q_norm.gamma"], c.qk_eps)
+        ckd = rms_norm(heads(sl(kv, 1), Ctx), Wd[pfx + "cross.k_norm.gamma"], c.qk_eps)
+        cv = heads(sl(kv, 2), Ctx)
+        oc = attn(cq, ck, cv, None) - attn(cqd, ckd, cv, None)
+    else:
+        cv = heads(sl(kv, 1), Ctx)
+        oc = attn(cq, ck, cv, None)
+    oc = lin(Wd, lora, pfx + "cross.out.weight", oc)
+    x = x + oc
+
+    res = x
+    f = rms_norm(x, Wd[pfx + "ff_norm.gamma"], c.norm_eps) * (1.0 + sc_f) + sh_f
+    f = lin(Wd, lora, pfx + "ff.proj.weight", f, Wd[pfx + "ff.proj.bias"])
+    inner = f.shape[1] // 2
+    f = f[:, :inner] * silu(f[:, inner:])
+    f = lin(Wd, lora, pfx + "ff.out.weight", f, Wd[pfx + "ff.out.bias"])
+    return res + gate(f, g_f)
+
+
+def mlp_silu(Wd, lora, pfx, x, bias):
+    h = lin(Wd, lora, pfx + "0.weight", x, Wd[pfx + "0.bias"] if bias else None)
+    return lin(Wd, lora, pfx + "2.weight", silu(h), Wd[pfx + "2.bias"] if bias else None)
+
+
+def dit_head(Wd, lora, x_in, t_feat, cross, glob, c: DitCfg):
+    """src/dit.h:286-310: returns (x0[mem+T][dim], context[Ctx][dim], gcond[6*dim])."""
+    torch = _torch()
+    te = mlp_silu(Wd, lora, "dit.time_embed.", t_feat, True)
+    g = mlp_silu(Wd, lora, "dit.global_embed.", glob, False) + te
+    gcond = mlp_silu(Wd, lora, "dit.gce.", g, True)
+    context = mlp_silu(Wd, lora, "dit.cond_embed.", cross, False)
+    x = lin(Wd, lora, "dit.pre_conv.weight", x_in) + x_in
+    x = lin(Wd, lora, "dit.proj_in.weight", x)
+    return torch.cat([Wd["dit.memory_tokens"], x], 0), context, gcond
+
+
+def dit_tail(Wd, lora, x, c: DitCfg):
+    """src/dit.h:314-323: drop memory tokens, proj_out, residual post_conv -> [T][io]."""
+    x = x[c.mem_tokens:]
+    x = lin(Wd, lora, "dit.proj_out.weight", x)
+    return lin(Wd, lora, "dit.post_conv.weight", x) + x
+
+
+def dit_loss(Wd, lora, x_t, t_feat, cross, glob, target, c: DitCfg, window=None):
+    """One sample's loss: mean((v - target)^2) over io*frames (src/train_ckpt.h:226-228)."""
+    torch = _torch()
+    x0, context, gcond = dit_head(Wd, lora, x_t, t_feat, cross, glob, c)
+    pos = torch.arange(x0.shape[0])
+    x = x0
+    for l in range(c.depth):
+        x = dit_block(Wd, lora, f"dit.{l}.", x, context, gcond, pos, c, window)
+    vel = dit_tail(Wd, lora, x, c)
+    d = vel - target
+    return (d * d).sum() / (c.io * target.shape[0])
+
+
+# --------------------------------------------------------------------------------------------
+# optimizer side (src/train_loop.h:147-211, src/train_optimizer.h:42-65)
+# --------------------------------------------------------------------------------------------
+def average_and_clip(grads, count, grad_clip):
+    """In place over a list of float32 arrays.  Returns the pre-clip global norm (f64)."""
+    if count > 1:
+        inv = np.float32(1.0) / np.float32(count)
+        for g in grads:
+            g *= inv
+    sumsq = 0.0
+    for g in grads:
+        sumsq += float(np.dot(g.astype(np.float64).ravel(), g.astype(np.float64).ravel()))
+    norm = math.sqrt(sumsq)
+    if grad_clip > 0.0 and norm > grad_clip:
+        scale = np.float32(grad_clip / (norm + 1e-6))
+        for g in grads:
+            g *= scale
+    return norm
+
+
+def adamw_f32(p, g, m, v, lr, b1, b2, eps, wd, step):
+    """In-place float32 restatement of adamw_update_vector (src/train_optimizer.h:42-65)."""
+    f = np.float32
+    b1c = f(1.0) - f(math.pow(f(b1), f(step)))
+    b2c = f(1.0) - f(math.pow(f(b2), f(step)))
+    m[...] = f(b1) * m + (f(1.0) - f(b1)) * g
+    v[...] = f(b2) * v + (f(1.0) - f(b2)) * g * g
+    mh = m / b1c
+    vh = v / b2c
+    p[...] = p - f(lr) * (mh / (np.sqrt(vh) + f(eps)) + f(wd) * p)
