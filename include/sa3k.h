@@ -1,0 +1,136 @@
+/*
+ * sa3k.h -- C ABI of the B200 (sm_100a) adapter-training hot path of sa3.cpp.
+ *
+ * Conventions follow the reference's libsa3 C ABI (src/libsa3.h:4-9): every call returns an int
+ * status (0 = OK), failures fill `err` (a caller buffer of `err_len` bytes), no C++ exception
+ * crosses the boundary, objects the library allocates are released by the library, and a
+ * context is bound to one device and one CUDA stream and is not reentrant.
+ *
+ * Tensors are passed as plain pointers with the ggml layout of the reference, i.e. ggml
+ * [ne0, ne1] = row-major [ne1][ne0]:
+ *   W [in, out]  -> W[out][in], quantized blocks along `in`      (frozen base weight)
+ *   x [in, S]    -> x[S][in]                                     (activations, f32)
+ *   A [in, r]    -> A[r][in]          B [r, out] -> B[out][r]    (TrainLoraParam layout,
+ *                                                                 src/train_lora.h:26-27)
+ * Unless a name ends in _host, pointers are DEVICE pointers on the context's device.
+ *
+ * There is no CPU fallback: without an sm_100 device every call fails with an error.
+ */
+#ifndef SA3K_H
+#define SA3K_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SA3K_TYPE_F32 0
+#define SA3K_TYPE_F16 1
+#define SA3K_TYPE_Q8_0 8
+#define SA3K_TYPE_Q4_K 12
+
+typedef struct sa3k_ctx sa3k_ctx;
+typedef struct sa3k_weight sa3k_weight;
+
+/* Library version string.  Counterpart of sa3_version (src/libsa3.h:188). */
+const char* sa3k_version(void);
+
+/* Bind a context to CUDA device `device` (must be sm_100) with a private stream.
+ * Replaces backend selection, make_backend (src/gguf_model.h:120-198). */
+int sa3k_ctx_create(int device, sa3k_ctx** out, char* err, int err_len);
+void sa3k_ctx_destroy(sa3k_ctx* ctx);
+
+/* Run subsequent work on `cuda_stream` (a cudaStream_t of the context's device; NULL restores
+ * the private stream).  No counterpart in the reference (ggml owns its streams). */
+int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len);
+
+/* Wait for the context's stream and report any asynchronous or device-side error (a bounded
+ * wait that timed out inside a kernel is reported here and cleared).
+ * Counterpart of the implicit sync in ggml_backend_tensor_get (src/train_loop.h:371). */
+int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len);
+
+/* Upload one frozen base weight from raw GGUF row bytes (host memory), ggml type
+ * F32 / F16 / Q8_0 / Q4_K, and repack it for the tensor-core engine.  `in` must be a multiple of
+ * 64 (Q8_0) or 256 (Q4_K).  Replaces the weight upload of load_gguf (src/gguf_model.h:318-329). */
+int sa3k_weight_upload(sa3k_ctx* ctx, int ggml_type, const void* blocks_host, int64_t in,
+                       int64_t out, sa3k_weight** w, char* err, int err_len);
+void sa3k_weight_free(sa3k_weight* w);
+
+/* dst[out][in] (f32) = the dequantized weight, bit-identical to ggml's to_float.
+ * Counterpart of read_to_f32 (src/lora.h:52-74). */
+int sa3k_dequant(sa3k_ctx* ctx, const sa3k_weight* w, float* dst, char* err, int err_len);
+
+/* Per output row: base_norm_sq[o] = sum_i W[o][i]^2 + in*eps and norm[o] = sqrt(sum_i W^2),
+ * f64 accumulation (either output may be NULL).  Replaces train_row_norm_sq and
+ * train_row_norms (src/train_lora.h:141-174) for the DoRA constants and magnitude init. */
+int sa3k_row_norms(sa3k_ctx* ctx, const sa3k_weight* w, float eps, float* base_norm_sq,
+                   float* norm, char* err, int err_len);
+
+/* One functional adapter on a linear, as DitLoraParam (src/dit.h:65-88). rank <= 16. */
+typedef struct sa3k_adapter {
+  const float* A;             /* [rank][in]                                   */
+  const float* B;             /* [out][rank]                                  */
+  const float* magnitude;     /* [out] for dora-rows, else NULL                */
+  const float* base_norm_sq;  /* [out] for dora-rows (sa3k_row_norms), else NULL */
+  float scale;                /* alpha / rank                                 */
+  int rank;
+} sa3k_adapter;
+
+/* y[S][out] = dit_lin(W, x) with the adapter (NULL: plain mul_mat) and optional bias[out]:
+ *   y = g * (x W^T + s (x A^T) B^T) + bias,  g = m / |W + s B A|_row (dora-rows) or 1.
+ * Replaces dit_lin (src/dit.h:92-149). */
+int sa3k_linear_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad,
+                    const float* bias, const float* x, int64_t S, float* y, char* err, int err_len);
+
+/* Backward of sa3k_linear_fwd for upstream dy[S][out], given its inputs x and its output y.
+ * Writes dx[S][in] (if non-NULL) and the adapter gradients dA[rank][in], dB[out][rank],
+ * dm[out] (dora; each may be NULL when ad is NULL).  accumulate != 0 adds into dx/dA/dB/dm
+ * instead of overwriting (gradient accumulation across samples / residual branches).
+ * Replaces the OUT_PROD / MUL_MAT backward that ggml_build_backward_expand derives for dit_lin
+ * (src/train_ckpt.h:400). */
+int sa3k_linear_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad,
+                    const float* bias, const float* x, const float* y, const float* dy, int64_t S,
+                    float* dx, float* dA, float* dB, float* dm, int accumulate, char* err,
+                    int err_len);
+
+/* Forward + backward of one adapted linear in one call (shares u = x A^T and the DoRA norm
+ * between the two passes).  Outputs y, dx, dA, dB, dm as above. */
+int sa3k_linear_fwd_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad,
+                        const float* bias, const float* x, const float* dy, int64_t S, float* y,
+                        float* dx, float* dA, float* dB, float* dm, char* err, int err_len);
+
+/* The same step with HOST buffers: copies x, dy and the adapter in, runs forward + backward and
+ * copies y, dx, dA, dB, dm out (all host pointers; A/B/magnitude/base_norm_sq in `ad` are host
+ * pointers too).  Mirrors what the reference does per step around ggml (tensor_set / graph
+ * compute / tensor_get, src/train_loop.h:331-371). */
+int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad_host,
+                             const float* bias_host, const float* x_host, const float* dy_host,
+                             int64_t S, float* y_host, float* dx_host, float* dA_host,
+                             float* dB_host, float* dm_host, char* err, int err_len);
+
+/* AdamW hyper-parameters, as TrainAdamWParams (src/train_optimizer.h:28-35). */
+typedef struct sa3k_adamw_params {
+  float learning_rate, beta1, beta2, eps, weight_decay, grad_clip;
+} sa3k_adamw_params;
+
+/* One AdamW update of n parameters with gradient g and moments m, v (updated in place), at
+ * optimizer step `step` (>= 1).  Bit-identical to adamw_update_vector
+ * (src/train_optimizer.h:42-65) for the same inputs. */
+int sa3k_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, float* v, int64_t n,
+               const sa3k_adamw_params* hp, int step, char* err, int err_len);
+
+/* train_apply_accumulated_adamw over flat buffers (src/train_loop.h:147-211): average the
+ * accumulated gradient g (n values, `count` samples), clip it to global L2 norm hp->grad_clip
+ * (f64 norm; 0 disables), then AdamW.  g is left unmodified.  grad_norm_out (host, nullable)
+ * receives the pre-clip norm; it forces a stream sync when requested. */
+int sa3k_average_clip_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, float* v,
+                            int64_t n, int count, const sa3k_adamw_params* hp, int step,
+                            double* grad_norm_out, char* err, int err_len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SA3K_H */

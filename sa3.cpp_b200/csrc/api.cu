@@ -1,0 +1,517 @@
+// api.cu -- the sa3k C ABI (include/sa3k.h): contexts, weights, dit_lin forward / backward and
+// the optimizer, orchestrated over the tcgen05 GEMM engine and the small kernels.
+#include "../../include/sa3k.h"
+#include "lora_kernels.h"
+#include "sa3k_internal.h"
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+struct sa3k_ctx {
+  sa3k::Ctx c;
+};
+struct sa3k_weight {
+  sa3k::Weight w;
+};
+
+namespace sa3k {
+
+static int fill_err(char* err, int len, const std::string& msg) {
+  if (err && len > 0) {
+    std::strncpy(err, msg.c_str(), (size_t)len - 1);
+    err[len - 1] = 0;
+  }
+  return 1;
+}
+
+void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err) {
+  if ((int)c->scratch.size() <= slot) c->scratch.resize((size_t)slot + 1);
+  Scratch& s = c->scratch[(size_t)slot];
+  if (s.bytes < bytes) {
+    if (s.ptr) {
+      cudaStreamSynchronize(c->stream);
+      cudaFree(s.ptr);
+      s.ptr = nullptr;
+      s.bytes = 0;
+    }
+    const size_t want = (bytes + 255) & ~(size_t)255;
+    if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
+      cudaGetLastError();
+      err = "out of device memory for scratch";
+      return nullptr;
+    }
+    s.bytes = want;
+  }
+  return s.ptr;
+}
+
+// Scratch slots of the linear path.
+enum Slot : int {
+  kS_XBF = 0, kS_ABF, kS_ATX, kS_BX, kS_BTBF, kS_U, kS_EXTU, kS_UT, kS_PT, kS_AAT, kS_NSQ, kS_G,
+  kS_DZ, kS_DG, kS_DU, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_Y, kS_HOST_IO, kS_OPT,
+  kS_COUNT
+};
+
+static int64_t pad64(int64_t v) { return (v + 63) / 64 * 64; }
+
+struct LinBufs {
+  __nv_bfloat16 *x_bf = nullptr, *a_bf = nullptr, *at_x = nullptr, *b_x = nullptr, *bt_bf = nullptr;
+  __nv_bfloat16 *ext_u = nullptr, *ut = nullptr, *dz = nullptr, *ext_du = nullptr, *dut = nullptr, *cb = nullptr;
+  float *u = nullptr, *pt = nullptr, *aat = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *du = nullptr,
+        *c3 = nullptr;
+  int64_t s_pad = 0;
+};
+
+template <class T>
+static bool get(Ctx* c, int slot, int64_t count, T*& p, std::string& err) {
+  p = static_cast<T*>(scratch_get(c, slot, (size_t)count * sizeof(T), err));
+  return p != nullptr;
+}
+
+static int lin_bufs(Ctx* c, int64_t S, int64_t in, int64_t out, bool adapter, bool dora, bool bwd,
+                    LinBufs& b, std::string& err) {
+  b.s_pad = pad64(S);
+  if (!get(c, kS_XBF, S * in, b.x_bf, err)) return 1;
+  if (adapter) {
+    if (!get(c, kS_ABF, 16 * in, b.a_bf, err) || !get(c, kS_ATX, in * 64, b.at_x, err) ||
+        !get(c, kS_BX, out * 64, b.b_x, err) || !get(c, kS_BTBF, 16 * out, b.bt_bf, err) ||
+        !get(c, kS_U, S * 16, b.u, err) || !get(c, kS_EXTU, S * 64, b.ext_u, err) ||
+        !get(c, kS_UT, 16 * b.s_pad, b.ut, err))
+      return 1;
+  }
+  if (dora) {
+    if (!get(c, kS_PT, 16 * out, b.pt, err) || !get(c, kS_AAT, 256, b.aat, err) ||
+        !get(c, kS_NSQ, out, b.nsq, err) || !get(c, kS_G, out, b.g, err))
+      return 1;
+  }
+  if (bwd) {
+    if (!get(c, kS_DZ, S * out, b.dz, err)) return 1;
+    if (dora && (!get(c, kS_DG, out, b.dg, err) || !get(c, kS_CB, 16 * out, b.cb, err) ||
+                 !get(c, kS_C3, 256, b.c3, err)))
+      return 1;
+    if (adapter && (!get(c, kS_DU, S * 16, b.du, err) || !get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
+                    !get(c, kS_DUT, 16 * b.s_pad, b.dut, err)))
+      return 1;
+  }
+  return 0;
+}
+
+// The shared body of linear forward / backward.  y_out: forward output (nullable = no forward);
+// y_in: the forward output consumed by the DoRA backward when no forward runs here.
+static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const float* bias, const float* x,
+                      const float* dy, int64_t S, float* y_out, const float* y_in, float* dx, float* dA,
+                      float* dB, float* dm, int accumulate, std::string& err) {
+  const int64_t in = w->in, out = w->out;
+  const bool adapter = ad != nullptr;
+  const bool dora = adapter && ad->magnitude != nullptr;
+  const bool fwd = y_out != nullptr;
+  const bool bwd = dy != nullptr;
+  if (S <= 0) { err = "S must be positive"; return 1; }
+  if (in % 64 != 0) { err = "in must be a multiple of 64"; return 1; }
+  if (adapter && (ad->rank < 1 || ad->rank > 16 || !ad->A || !ad->B)) { err = "adapter rank must be 1..16 with A and B"; return 1; }
+  if (dora && !ad->base_norm_sq) { err = "dora adapter needs base_norm_sq"; return 1; }
+  if (bwd && !fwd && dora && !y_in) { err = "dora backward needs the forward output y"; return 1; }
+  const int rank = adapter ? ad->rank : 0;
+  const float s = adapter ? ad->scale : 0.f;
+  LinBufs b;
+  if (lin_bufs(c, S, in, out, adapter, dora, bwd, b, err)) return 1;
+
+  if (k_cvt_bf16(c, x, S * in, b.x_bf, err)) return 1;
+  if (adapter) {
+    if (k_prep_adapter(c, ad->A, ad->B, rank, in, out, b.a_bf, b.at_x, b.b_x, b.bt_bf, err)) return 1;
+    // u = x A^T  [S][16]
+    GemmDesc g;
+    g.M = (int)S; g.N = 16; g.K = (int)in;
+    g.a = b.x_bf; g.lda = in;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.a_bf; g.ldb = in;
+    g.out = b.u; g.ldo = 16; g.bn = 16;
+    if (gemm(c, g, err)) return 1;
+    if (k_pack_rank(c, b.u, (int)S, s, b.ext_u, 1.0f, bwd ? b.ut : nullptr, (int)b.s_pad, err)) return 1;
+  }
+  if (dora) {
+    // P^T = A W^T  [16][out] ; then the row norm and g = m / sqrt(nsq)
+    GemmDesc g;
+    g.M = 16; g.N = (int)out; g.K = (int)in;
+    g.a = b.a_bf; g.lda = in;
+    g.bsrc = kB_WEIGHT_NT; g.w = w;
+    g.out = b.pt; g.ldo = out;
+    if (gemm(c, g, err)) return 1;
+    if (k_aat(c, ad->A, rank, in, b.aat, err)) return 1;
+    if (k_dora_norm(c, b.pt, ad->B, rank, out, b.aat, ad->base_norm_sq, ad->magnitude, s, b.nsq, b.g, err)) return 1;
+  }
+  if (fwd) {
+    GemmDesc g;
+    g.M = (int)S; g.N = (int)out; g.K = (int)in;
+    g.a = b.x_bf; g.lda = in;
+    g.bsrc = kB_WEIGHT_NT; g.w = w;
+    if (adapter) { g.ext_a = b.ext_u; g.ext_b = b.b_x; }
+    g.col_scale = dora ? b.g : nullptr;
+    g.col_bias = bias;
+    g.out = y_out; g.ldo = out;
+    if (gemm(c, g, err)) return 1;
+  }
+  if (!bwd) return 0;
+
+  const float* y_used = fwd ? y_out : y_in;
+  if (dora && cudaMemsetAsync(b.dg, 0, sizeof(float) * out, c->stream) != cudaSuccess) return check_launch("memset", err);
+  if (k_bwd_prologue(c, dy, dora ? y_used : nullptr, bias, dora ? b.g : nullptr, S, out, b.dz, dora ? b.dg : nullptr, err))
+    return 1;
+  if (adapter) {
+    // du = s dz B  [S][16]
+    GemmDesc g;
+    g.M = (int)S; g.N = 16; g.K = (int)out;
+    g.a = b.dz; g.lda = out;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.bt_bf; g.ldb = out;
+    g.alpha = s;
+    g.out = b.du; g.ldo = 16; g.bn = 16;
+    if (gemm(c, g, err)) return 1;
+    if (k_pack_rank(c, b.du, (int)S, 1.0f, b.ext_du, 1.0f, b.dut, (int)b.s_pad, err)) return 1;
+  }
+  if (dx) {
+    // dx = dz W + du A  (the LoRA term as a K = 16 extension of the same MMA chain)
+    GemmDesc g;
+    g.M = (int)S; g.N = (int)in; g.K = (int)out;
+    g.a = b.dz; g.lda = out;
+    g.bsrc = kB_WEIGHT_TN; g.w = w;
+    if (adapter) { g.ext_a = b.ext_du; g.ext_b = b.at_x; }
+    g.out = dx; g.ldo = in; g.accumulate = accumulate;
+    if (gemm(c, g, err)) return 1;
+  }
+  if (!adapter) return 0;
+  {
+    // dB = s dz^T u  [out][rank]
+    GemmDesc g;
+    g.M = (int)out; g.N = rank; g.K = (int)S;
+    g.a = b.dz; g.lda = out; g.a_mn = 1;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.ut; g.ldb = b.s_pad;
+    g.alpha = s;
+    g.out = dB; g.ldo = rank; g.accumulate = accumulate; g.bn = 16;
+    if (gemm(c, g, err)) return 1;
+  }
+  {
+    // dA = du^T x  [rank][in]
+    GemmDesc g;
+    g.M = rank; g.N = (int)in; g.K = (int)S;
+    g.a = b.dut; g.lda = b.s_pad;
+    g.bsrc = kB_BF16_MNMAJOR; g.b = b.x_bf; g.ldb = in;
+    g.out = dA; g.ldo = in; g.accumulate = accumulate;
+    if (gemm(c, g, err)) return 1;
+  }
+  if (dora) {
+    if (cudaMemsetAsync(b.c3, 0, sizeof(float) * 256, c->stream) != cudaSuccess) return check_launch("memset", err);
+    if (k_dora_bwd(c, b.pt, ad->B, rank, out, b.aat, b.nsq, b.g, b.dg, s, dm, accumulate, dB, b.cb, b.c3, err)) return 1;
+    GemmDesc g;
+    g.M = rank; g.N = (int)in; g.K = (int)out;
+    g.a = b.cb; g.lda = out;
+    g.bsrc = kB_WEIGHT_TN; g.w = w;
+    g.out = dA; g.ldo = in; g.accumulate = 1;
+    if (gemm(c, g, err)) return 1;
+    if (k_dora_da_c3(c, b.c3, ad->A, rank, in, dA, err)) return 1;
+  }
+  return 0;
+}
+
+static int adamw_bias_corrections(const sa3k_adamw_params* hp, int step, float& b1c, float& b2c) {
+  // exactly the reference's float expressions (src/train_optimizer.h:55-56)
+  b1c = 1.0f - std::pow(hp->beta1, (float)step);
+  b2c = 1.0f - std::pow(hp->beta2, (float)step);
+  return 0;
+}
+
+}  // namespace sa3k
+
+using namespace sa3k;
+
+extern "C" {
+
+const char* sa3k_version(void) { return "sa3k 0.1.0 (sm_100a)"; }
+
+int sa3k_ctx_create(int device, sa3k_ctx** out, char* err, int err_len) {
+  if (!out) return fill_err(err, err_len, "out is NULL");
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return fill_err(err, err_len, "no CUDA device available (sa3k has no CPU fallback)");
+  }
+  if (device < 0 || device >= n) return fill_err(err, err_len, "device ordinal out of range");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return fill_err(err, err_len, "cudaGetDeviceProperties failed");
+  if (prop.major != 10) return fill_err(err, err_len, "sa3k kernels are built for sm_100a (B200); device is sm_" +
+                                                          std::to_string(prop.major) + std::to_string(prop.minor));
+  if (cudaSetDevice(device) != cudaSuccess) return fill_err(err, err_len, "cudaSetDevice failed");
+  sa3k_ctx* c = new (std::nothrow) sa3k_ctx();
+  if (!c) return fill_err(err, err_len, "out of host memory");
+  c->c.device = device;
+  c->c.sm_count = (size_t)prop.multiProcessorCount;
+  if (cudaStreamCreateWithFlags(&c->c.stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaMalloc(&c->c.d_err, sizeof(int)) != cudaSuccess || cudaMemset(c->c.d_err, 0, sizeof(int)) != cudaSuccess) {
+    delete c;
+    return fill_err(err, err_len, "failed to create the context stream / error word");
+  }
+  c->c.own_stream = true;
+  *out = c;
+  return 0;
+}
+
+void sa3k_ctx_destroy(sa3k_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->c.device);
+  cudaStreamSynchronize(ctx->c.stream);
+  for (auto& s : ctx->c.scratch)
+    if (s.ptr) cudaFree(s.ptr);
+  if (ctx->c.d_err) cudaFree(ctx->c.d_err);
+  if (ctx->c.own_stream) cudaStreamDestroy(ctx->c.stream);
+  delete ctx;
+}
+
+int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* stream, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  if (!stream) {
+    if (!ctx->c.own_stream) {
+      if (cudaStreamCreateWithFlags(&ctx->c.stream, cudaStreamNonBlocking) != cudaSuccess)
+        return fill_err(err, err_len, "failed to create stream");
+      ctx->c.own_stream = true;
+    }
+    return 0;
+  }
+  if (ctx->c.own_stream) {
+    cudaStreamSynchronize(ctx->c.stream);
+    cudaStreamDestroy(ctx->c.stream);
+  }
+  ctx->c.stream = static_cast<cudaStream_t>(stream);
+  ctx->c.own_stream = false;
+  return 0;
+}
+
+int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  cudaSetDevice(ctx->c.device);
+  cudaError_t e = cudaStreamSynchronize(ctx->c.stream);
+  if (e != cudaSuccess) return fill_err(err, err_len, std::string("CUDA error: ") + cudaGetErrorString(e));
+  int code = 0;
+  if (cudaMemcpy(&code, ctx->c.d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fill_err(err, err_len, "failed to read the device error word");
+  if (code != 0) {
+    cudaMemset(ctx->c.d_err, 0, sizeof(int));
+    return fill_err(err, err_len, "device wait timed out inside a kernel (code " + std::to_string(code) + ")");
+  }
+  return 0;
+}
+
+int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, int64_t out, sa3k_weight** wout,
+                       char* err, int err_len) {
+  if (!ctx || !blocks || !wout) return fill_err(err, err_len, "NULL argument");
+  *wout = nullptr;
+  if (in <= 0 || out <= 0) return fill_err(err, err_len, "weight dims must be positive");
+  if (in % 64 != 0) return fill_err(err, err_len, "weight `in` must be a multiple of 64");
+  size_t raw_bytes = 0;
+  switch (type) {
+    case kTypeF32: raw_bytes = (size_t)(in * out * 4); break;
+    case kTypeF16: raw_bytes = (size_t)(in * out * 2); break;
+    case kTypeQ8_0: raw_bytes = (size_t)(in / 32 * 34 * out); break;
+    case kTypeQ4_K:
+      if (in % 256 != 0) return fill_err(err, err_len, "Q4_K needs `in` to be a multiple of 256");
+      raw_bytes = (size_t)(in / 256 * 144 * out);
+      break;
+    default: return fill_err(err, err_len, "unsupported ggml type (F32, F16, Q8_0, Q4_K)");
+  }
+  cudaSetDevice(ctx->c.device);
+  sa3k_weight* h = new (std::nothrow) sa3k_weight();
+  if (!h) return fill_err(err, err_len, "out of host memory");
+  Weight& w = h->w;
+  w.type = type; w.in = in; w.out = out; w.owner = &ctx->c;
+  std::string e;
+  auto fail = [&](const std::string& msg) {
+    if (w.raw) cudaFree(w.raw);
+    if (w.codes) cudaFree(w.codes);
+    if (w.scales) cudaFree(w.scales);
+    if (w.bf16) cudaFree(w.bf16);
+    delete h;
+    cudaGetLastError();
+    return fill_err(err, err_len, msg);
+  };
+  if (cudaMalloc(&w.raw, raw_bytes) != cudaSuccess) return fail("out of device memory (weight)");
+  if (cudaMemcpyAsync(w.raw, blocks, raw_bytes, cudaMemcpyHostToDevice, ctx->c.stream) != cudaSuccess)
+    return fail("weight upload copy failed");
+  if (type == kTypeQ8_0) {
+    if (cudaMalloc(&w.codes, (size_t)(in * out)) != cudaSuccess ||
+        cudaMalloc(&w.scales, (size_t)(in / 32 * out * 4)) != cudaSuccess)
+      return fail("out of device memory (weight)");
+  } else if (type == kTypeQ4_K) {
+    if (cudaMalloc(&w.codes, (size_t)(in / 2 * out)) != cudaSuccess ||
+        cudaMalloc(&w.scales, (size_t)(in / 32 * out * 8)) != cudaSuccess)
+      return fail("out of device memory (weight)");
+  } else {
+    if (cudaMalloc(&w.bf16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight)");
+  }
+  if (weight_repack(&ctx->c, &w, e)) return fail(e);
+  if (cudaStreamSynchronize(ctx->c.stream) != cudaSuccess) return fail("weight repack failed");
+  if (type == kTypeQ8_0 || type == kTypeQ4_K) {   // codes + scales carry every bit of the blocks
+    cudaFree(w.raw);
+    w.raw = nullptr;
+  }
+  *wout = h;
+  return 0;
+}
+
+void sa3k_weight_free(sa3k_weight* h) {
+  if (!h) return;
+  Weight& w = h->w;
+  if (w.owner) {
+    cudaSetDevice(w.owner->device);
+    cudaStreamSynchronize(w.owner->stream);
+  }
+  if (w.raw) cudaFree(w.raw);
+  if (w.codes) cudaFree(w.codes);
+  if (w.scales) cudaFree(w.scales);
+  if (w.bf16) cudaFree(w.bf16);
+  delete h;
+}
+
+int sa3k_dequant(sa3k_ctx* ctx, const sa3k_weight* w, float* dst, char* err, int err_len) {
+  if (!ctx || !w || !dst) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (weight_dequant(&ctx->c, &w->w, dst, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_row_norms(sa3k_ctx* ctx, const sa3k_weight* w, float eps, float* nsq, float* nrm, char* err, int err_len) {
+  if (!ctx || !w) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (weight_row_norms(&ctx->c, &w->w, eps, nsq, nrm, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad, const float* bias,
+                    const float* x, int64_t S, float* y, char* err, int err_len) {
+  if (!ctx || !w || !x || !y) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (linear_run(&ctx->c, &w->w, ad, bias, x, nullptr, S, y, nullptr, nullptr, nullptr, nullptr, nullptr, 0, e))
+    return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad, const float* bias,
+                    const float* x, const float* y, const float* dy, int64_t S, float* dx, float* dA, float* dB,
+                    float* dm, int accumulate, char* err, int err_len) {
+  if (!ctx || !w || !x || !dy) return fill_err(err, err_len, "NULL argument");
+  if (ad && (!dA || !dB || (ad->magnitude && !dm))) return fill_err(err, err_len, "adapter gradients need dA, dB (and dm)");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (linear_run(&ctx->c, &w->w, ad, bias, x, dy, S, nullptr, y, dx, dA, dB, dm, accumulate, e))
+    return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_fwd_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad, const float* bias,
+                        const float* x, const float* dy, int64_t S, float* y, float* dx, float* dA, float* dB,
+                        float* dm, char* err, int err_len) {
+  if (!ctx || !w || !x || !dy || !y) return fill_err(err, err_len, "NULL argument");
+  if (ad && (!dA || !dB || (ad->magnitude && !dm))) return fill_err(err, err_len, "adapter gradients need dA, dB (and dm)");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (linear_run(&ctx->c, &w->w, ad, bias, x, dy, S, y, nullptr, dx, dA, dB, dm, 0, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* adh, const float* bias_h,
+                             const float* x_h, const float* dy_h, int64_t S, float* y_h, float* dx_h, float* dA_h,
+                             float* dB_h, float* dm_h, char* err, int err_len) {
+  if (!ctx || !w || !x_h || !dy_h || !y_h) return fill_err(err, err_len, "NULL argument");
+  Ctx* c = &ctx->c;
+  cudaSetDevice(c->device);
+  const int64_t in = w->w.in, out = w->w.out;
+  const int rank = adh ? adh->rank : 0;
+  const bool dora = adh && adh->magnitude;
+  // one device block: x, dy, y, dx, A, B, m, bns, bias, dA, dB, dm
+  const int64_t n_x = S * in, n_dy = S * out;
+  const int64_t n_a = (int64_t)rank * in, n_b = out * rank;
+  const int64_t total = 2 * n_x + 2 * n_dy + 2 * n_a + 2 * n_b + 4 * out + 64;
+  std::string e;
+  float* base = static_cast<float*>(scratch_get(c, kS_HOST_IO, (size_t)total * sizeof(float), e));
+  if (!base) return fill_err(err, err_len, e);
+  auto take = [&](int64_t n) { float* p = base; base += (n + 15) / 16 * 16; return p; };
+  float *x = take(n_x), *dy = take(n_dy), *y = take(n_dy), *dx = take(n_x);
+  float *A = take(n_a), *B = take(n_b), *m = take(out), *bns = take(out), *bias = take(out);
+  float *dA = take(n_a), *dB = take(n_b), *dm = take(out);
+  const cudaStream_t st = c->stream;
+  auto h2d = [&](float* d, const float* h, int64_t n) {
+    return cudaMemcpyAsync(d, h, (size_t)n * sizeof(float), cudaMemcpyHostToDevice, st) == cudaSuccess;
+  };
+  auto d2h = [&](float* h, const float* d, int64_t n) {
+    return cudaMemcpyAsync(h, d, (size_t)n * sizeof(float), cudaMemcpyDeviceToHost, st) == cudaSuccess;
+  };
+  bool ok = h2d(x, x_h, n_x) && h2d(dy, dy_h, n_dy);
+  if (bias_h) ok = ok && h2d(bias, bias_h, out);
+  sa3k_adapter ad{};
+  if (adh) {
+    ok = ok && h2d(A, adh->A, n_a) && h2d(B, adh->B, n_b);
+    if (dora) ok = ok && h2d(m, adh->magnitude, out) && h2d(bns, adh->base_norm_sq, out);
+    ad.A = A; ad.B = B; ad.magnitude = dora ? m : nullptr; ad.base_norm_sq = dora ? bns : nullptr;
+    ad.scale = adh->scale; ad.rank = rank;
+  }
+  if (!ok) return fill_err(err, err_len, "host->device copy failed");
+  if (linear_run(c, &w->w, adh ? &ad : nullptr, bias_h ? bias : nullptr, x, dy, S, y, nullptr, dx_h ? dx : nullptr,
+                 adh ? dA : nullptr, adh ? dB : nullptr, dora ? dm : nullptr, 0, e))
+    return fill_err(err, err_len, e);
+  ok = d2h(y_h, y, n_dy);
+  if (dx_h) ok = ok && d2h(dx_h, dx, n_x);
+  if (adh) {
+    if (dA_h) ok = ok && d2h(dA_h, dA, n_a);
+    if (dB_h) ok = ok && d2h(dB_h, dB, n_b);
+    if (dora && dm_h) ok = ok && d2h(dm_h, dm, out);
+  }
+  if (!ok) return fill_err(err, err_len, "device->host copy failed");
+  if (cudaStreamSynchronize(st) != cudaSuccess) return fill_err(err, err_len, "linear step failed");
+  return 0;
+}
+
+int sa3k_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, float* v, int64_t n, const sa3k_adamw_params* hp,
+               int step, char* err, int err_len) {
+  if (!ctx || !p || !g || !m || !v || !hp) return fill_err(err, err_len, "NULL argument");
+  if (step <= 0) return fill_err(err, err_len, "AdamW step must be positive");
+  cudaSetDevice(ctx->c.device);
+  float b1c, b2c;
+  adamw_bias_corrections(hp, step, b1c, b2c);
+  std::string e;
+  if (k_adamw(&ctx->c, p, g, m, v, n, hp->learning_rate, hp->beta1, hp->beta2, hp->eps, hp->weight_decay, b1c, b2c,
+              nullptr, e))
+    return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_average_clip_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, float* v, int64_t n, int count,
+                            const sa3k_adamw_params* hp, int step, double* grad_norm_out, char* err, int err_len) {
+  if (!ctx || !p || !g || !m || !v || !hp) return fill_err(err, err_len, "NULL argument");
+  if (count <= 0) return fill_err(err, err_len, "cannot apply empty gradient batch");
+  if (step <= 0) return fill_err(err, err_len, "AdamW step must be positive");
+  Ctx* c = &ctx->c;
+  cudaSetDevice(c->device);
+  std::string e;
+  // [0]: f64 sum of squares, [1]: f64 norm, then 2 floats of scales
+  double* acc = static_cast<double*>(scratch_get(c, kS_OPT, 64, e));
+  if (!acc) return fill_err(err, err_len, e);
+  float* scales = reinterpret_cast<float*>(acc + 2);
+  const float inv = count > 1 ? 1.0f / (float)count : 1.0f;
+  if (cudaMemsetAsync(acc, 0, sizeof(double), c->stream) != cudaSuccess) return fill_err(err, err_len, "memset failed");
+  if (k_sumsq(c, g, n, inv, acc, e) || k_clip_scale(c, acc, hp->grad_clip, inv, scales, acc + 1, e))
+    return fill_err(err, err_len, e);
+  float b1c, b2c;
+  adamw_bias_corrections(hp, step, b1c, b2c);
+  if (k_adamw(c, p, g, m, v, n, hp->learning_rate, hp->beta1, hp->beta2, hp->eps, hp->weight_decay, b1c, b2c, scales, e))
+    return fill_err(err, err_len, e);
+  if (grad_norm_out) {
+    if (cudaMemcpyAsync(grad_norm_out, acc + 1, sizeof(double), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess ||
+        cudaStreamSynchronize(c->stream) != cudaSuccess)
+      return fill_err(err, err_len, "failed to read the gradient norm");
+  }
+  return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,177 @@
+// gemm_tc.cu -- host side of the tcgen05 GEMM engine: tensor maps, tile choice, launch.
+#include "gemm_tc.cuh"
+#include "sa3k_internal.h"
+
+#include <cstdio>
+#include <mutex>
+
+namespace sa3k {
+
+PFN_encodeTiled encode_tiled_fn(std::string& err) {
+  static PFN_encodeTiled fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_encodeTiled>(p);
+  });
+  if (!fn) err = "cuTensorMapEncodeTiled is unavailable (no CUDA driver)";
+  return fn;
+}
+
+// 2-D tensor map over a row-major [outer][inner] array with `row_bytes` between rows.
+static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                    uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                    CUtensorMapSwizzle sw, const char* what, std::string& err) {
+  PFN_encodeTiled enc = encode_tiled_fn(err);
+  if (!enc) return 1;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row_bytes & 15) != 0) {
+    err = std::string(what) + ": TMA needs 16-byte aligned base and row pitch";
+    return 1;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof buf, "%s: cuTensorMapEncodeTiled failed (%d) dims=%llu x %llu box=%u x %u",
+             what, (int)r, (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+    err = buf;
+    return 1;
+  }
+  return 0;
+}
+
+template <int BN, int STAGES, int BMODE, bool A_MN>
+static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtensorMap& tb,
+                  const CUtensorMap& tbs, const CUtensorMap& tea, const CUtensorMap& teb,
+                  const GemmArgs& args, std::string& err) {
+  using L = GemmSmem<BN, STAGES, BMODE>;
+  auto kern = gemm_tc_kernel<BN, STAGES, BMODE, A_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN) != cudaSuccess)
+      return check_launch("gemm smem attribute", err);
+    attr_set = true;
+  }
+  dim3 grid((unsigned)((d.M + kBM - 1) / kBM), (unsigned)((d.N + BN - 1) / BN));
+  kern<<<grid, kThreads, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, args);
+  return check_launch("gemm_tc", err);
+}
+
+int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
+  if (d.M <= 0 || d.N <= 0 || d.K < 0 || (d.K == 0 && !d.ext_a)) {
+    err = "gemm: need M, N > 0 and K > 0";
+    return 1;
+  }
+  const bool quant = (d.bsrc == kB_WEIGHT_NT || d.bsrc == kB_WEIGHT_TN) && d.w &&
+                     (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K);
+  const int bn = d.bn;
+  if (!(bn == 16 || bn == 128)) {
+    err = "gemm: unsupported N tile";
+    return 1;
+  }
+  if (quant && bn != 128) {
+    err = "gemm: quantized B needs the 128-wide N tile";
+    return 1;
+  }
+  CUtensorMap ta, tb, tbs, tea, teb;
+  memset(&tbs, 0, sizeof tbs);
+  memset(&tea, 0, sizeof tea);
+  memset(&teb, 0, sizeof teb);
+  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  const auto NOSW = CU_TENSOR_MAP_SWIZZLE_NONE;
+
+  if (d.a_mn) {
+    if (make_map(&ta, BF, d.a, d.M, d.K, d.lda * 2, 64, 64, SW, "A (MN-major)", err)) return 1;
+  } else {
+    if (make_map(&ta, BF, d.a, d.K, d.M, d.lda * 2, 64, kBM, SW, "A", err)) return 1;
+  }
+  int bmode = 0;
+  if (d.bsrc == kB_BF16_KMAJOR) {
+    bmode = 0;
+    if (make_map(&tb, BF, d.b, d.K, d.N, d.ldb * 2, 64, bn, SW, "B", err)) return 1;
+  } else if (d.bsrc == kB_BF16_MNMAJOR) {
+    bmode = 1;
+    if (make_map(&tb, BF, d.b, d.N, d.K, d.ldb * 2, 64, 64, SW, "B (MN-major)", err)) return 1;
+  } else {
+    const Weight* w = d.w;
+    const bool nt = d.bsrc == kB_WEIGHT_NT;
+    if (nt ? (w->out != d.N || w->in != d.K) : (w->out != d.K || w->in != d.N)) {
+      err = "gemm: weight shape does not match the GEMM";
+      return 1;
+    }
+    if (w->type == kTypeQ8_0) {
+      bmode = nt ? 2 : 3;
+      const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+      if (nt) {
+        if (make_map(&tb, U8, w->codes, w->in, w->out, w->in, 64, bn, NOSW, "Q8_0 codes", err)) return 1;
+        if (make_map(&tbs, F32, w->scales, w->out, w->in / 32, w->out * 4, bn, 2, NOSW, "Q8_0 scales", err)) return 1;
+      } else {
+        if (make_map(&tb, U8, w->codes, w->in, w->out, w->in, bn, 64, NOSW, "Q8_0 codes", err)) return 1;
+        if (make_map(&tbs, F32, w->scales, w->out, w->in / 32, w->out * 4, 64, bn / 32, NOSW, "Q8_0 scales", err)) return 1;
+      }
+    } else if (w->type == kTypeQ4_K) {
+      bmode = nt ? 4 : 5;
+      const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+      const auto U64 = CU_TENSOR_MAP_DATA_TYPE_UINT64;
+      if (nt) {
+        if (make_map(&tb, U8, w->codes, w->in / 2, w->out, w->in / 2, 32, bn, NOSW, "Q4_K codes", err)) return 1;
+        if (make_map(&tbs, U64, w->scales, w->out, w->in / 32, w->out * 8, bn, 2, NOSW, "Q4_K scales", err)) return 1;
+      } else {
+        if (make_map(&tb, U8, w->codes, w->in / 2, w->out, w->in / 2, bn / 2, 64, NOSW, "Q4_K codes", err)) return 1;
+        if (make_map(&tbs, U64, w->scales, w->out, w->in / 32, w->out * 8, 64, bn / 32, NOSW, "Q4_K scales", err)) return 1;
+      }
+    } else {
+      // F16 / F32 bases run on their bf16 copy
+      if (nt) {
+        bmode = 0;
+        if (make_map(&tb, BF, w->bf16, w->in, w->out, w->in * 2, 64, bn, SW, "W bf16", err)) return 1;
+      } else {
+        bmode = 1;
+        if (make_map(&tb, BF, w->bf16, w->in, w->out, w->in * 2, 64, 64, SW, "W^T bf16", err)) return 1;
+      }
+    }
+  }
+  if (d.ext_a) {
+    if (make_map(&tea, BF, d.ext_a, 64, d.M, 128, 64, kBM, SW, "ext A", err)) return 1;
+    if (make_map(&teb, BF, d.ext_b, 64, d.N, 128, 64, bn, SW, "ext B", err)) return 1;
+  } else {
+    tea = ta;
+    teb = tb;
+  }
+  if (bmode < 2) tbs = tb;   // unused by the kernel; keep it a valid map
+
+  GemmArgs a;
+  a.M = d.M; a.N = d.N; a.K = d.K;
+  a.has_ext = d.ext_a ? 1 : 0;
+  a.col_scale = d.col_scale; a.col_bias = d.col_bias; a.alpha = d.alpha;
+  a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
+  a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans;
+  a.err = c->d_err;
+
+  if (bn == 16) {
+    if (bmode != 0) { err = "gemm: N tile 16 supports bf16 K-major B only"; return 1; }
+    return d.a_mn ? launch<16, 8, 0, true>(c, d, ta, tb, tbs, tea, teb, a, err)
+                  : launch<16, 8, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+  }
+  if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
+  switch (bmode) {
+    case 0: return launch<128, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 1: return launch<128, 4, 1, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 2: return launch<128, 4, 2, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 3: return launch<128, 4, 3, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 4: return launch<128, 4, 4, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    default: return launch<128, 4, 5, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+  }
+}
+
+}  // namespace sa3k

@@ -1,0 +1,415 @@
+// gemm_tc.cuh -- the tcgen05 GEMM engine behind every contraction of the adapter-training path.
+//
+//   D[M x N] (f32, in TMEM) = sum_k Aop[m, k] * Bop[n, k]   (+ one optional K = 16 "extension")
+//
+// It replaces ggml's MUL_MAT / OUT_PROD for the calls of src/dit.h:107,120-121,132,136-137 and
+// their backward (ggml_build_backward_expand at src/train_ckpt.h:400).  One CTA computes one
+// 128 x BN output tile with a warp-specialized pipeline:
+//
+//   warp 0      TMA producer: A tile (bf16) + B tile (bf16) or the raw quantized B bytes + scales
+//   warp 1      TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16)
+//   warps 2-5   dequant stage (quantized B only): raw bytes -> bf16 in the 128B-swizzled UMMA
+//               layout, then the epilogue: tcgen05.ld of the accumulator -> scale/bias -> global
+//
+// Operand layouts in shared memory (bf16, 128-byte swizzle, BK = 64 = one swizzle row):
+//   K-major:  [rows][64] -- row r at r*128 B, 8-row groups of 1024 B (SBO = 1024);
+//             advancing K by 16 moves the start address by 32 B.
+//   MN-major: [64 k-rows][64 mn] atoms of 8 KB, atom j (mn 64j..) at j*8192 (LBO = 8192),
+//             8-k-row groups at 1024 B (SBO = 1024); advancing K by 16 moves by 2048 B.
+//
+// B operand modes (BMODE):
+//   0  bf16 K-major via TMA  ([N][K] row-major in HBM)
+//   1  bf16 MN-major via TMA ([K][N] row-major in HBM)
+//   2  Q8_0 "NT": W[out = N][in = K] quantized along K, dequantized K-major      (forward)
+//   3  Q8_0 "TN": W[out = K][in = N] quantized along N, dequantized MN-major     (dX = W^T dy)
+//   4  Q4_K "NT", 5  Q4_K "TN": as 2 / 3 with 4-bit codes.
+// Quantized weights live in HBM repacked by quant.cu: int8 codes (Q8_0) or natural-order nibble
+// pairs (Q4_K) as [out][in], and per-32-element scales as [in/32][out] f32 (Q8_0: d) or
+// float2 (Q4_K: d*sc, dmin*m) -- the same numbers the GGUF blocks encode, so the dequantized
+// values are bit-identical to ggml's to_float (then rounded once to bf16 for the tensor core).
+#pragma once
+
+#include "sa3k_common.cuh"
+
+namespace sa3k {
+
+struct GemmArgs {
+  int M, N, K;              // K: main reduction length (the last 64-block may be ragged)
+  int has_ext;              // add one K = 16 MMA from the extension operands
+  const float* col_scale;   // per-column multiplier (nullable)
+  const float* col_bias;    // per-column bias, added after scaling (nullable)
+  float alpha;              // global multiplier
+  float* out;               // f32 output (nullable)
+  long ldo;                 // its leading dimension (elements)
+  int out_trans;            // 0: out[m*ldo + n]; 1: out[n*ldo + m]
+  int accumulate;           // add into out instead of overwriting
+  __nv_bfloat16* out_bf;    // bf16 output (nullable), same scale/bias as out
+  long ldo_bf;
+  int out_bf_trans;
+  int* err;                 // device error word
+};
+
+constexpr int kBM = 128, kBK = 64;
+constexpr int kThreads = 192;
+
+template <int BMODE>
+struct BModeTraits {
+  static constexpr bool quant = BMODE >= 2;
+  static constexpr bool mn = (BMODE == 1 || BMODE == 3 || BMODE == 5);
+  static constexpr bool q8 = (BMODE == 2 || BMODE == 3);
+  static constexpr bool q4 = (BMODE == 4 || BMODE == 5);
+};
+
+__host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int BN, int STAGES, int BMODE>
+struct GemmSmem {
+  static constexpr int A_BYTES = kBM * kBK * 2;
+  static constexpr int B_BYTES = BN * kBK * 2;
+  static constexpr int RAW_BYTES =
+      BModeTraits<BMODE>::q8 ? BN * kBK : BModeTraits<BMODE>::q4 ? BN * kBK / 2 : 0;
+  static constexpr int SC_BYTES =
+      BModeTraits<BMODE>::q8 ? BN * 2 * 4 : BModeTraits<BMODE>::q4 ? BN * 2 * 8 : 0;
+  static constexpr int RAW_STRIDE = align_up(RAW_BYTES, 128);
+  static constexpr int SC_STRIDE = align_up(SC_BYTES, 128);
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_STRIDE;
+  static constexpr int OFF_BAR = align_up(OFF_SC + STAGES * SC_STRIDE, 64);
+  static constexpr int BAR_BYTES = (3 * STAGES + 1) * 8 + 16;
+  static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
+  static constexpr int DYN = TOTAL + 1024;   // slack for 1024-byte alignment of the base
+  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+};
+
+// ------------------------------------------------------------------ dequantization stages
+// Each of the 128 dequant threads writes BN/16 16-byte chunks (8 bf16) of the B stage.
+
+// Q8_0, K-major output [BN rows = out][64 k = in]; raw [BN][64] int8, sc [2][BN] f32.
+template <int BN>
+__device__ __forceinline__ void dequant_q8_nt(const uint8_t* raw, const float* sc, uint8_t* bst,
+                                              int tid) {
+#pragma unroll
+  for (int j = 0; j < BN / 16; ++j) {
+    const int idx = tid + 128 * j;
+    const int r = idx >> 3, c = idx & 7;
+    const uint2 q = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);
+    const float s = sc[(c >> 2) * BN + r];
+    uint4 o;
+    const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+    o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
+    o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
+    o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
+    o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
+    *reinterpret_cast<uint4*>(bst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
+  }
+}
+
+// Q8_0, MN-major output [64 k = out][BN n = in]; raw [64][BN] int8, sc [BN/32][64] f32.
+template <int BN>
+__device__ __forceinline__ void dequant_q8_tn(const uint8_t* raw, const float* sc, uint8_t* bst,
+                                              int tid) {
+  constexpr int CPR = BN / 8;   // chunks per k-row
+#pragma unroll
+  for (int j = 0; j < BN / 16; ++j) {
+    const int idx = tid + 128 * j;
+    const int k = idx / CPR, cn = idx % CPR;
+    const uint2 q = *reinterpret_cast<const uint2*>(raw + k * BN + cn * 8);
+    const float s = sc[(cn >> 2) * 64 + k];
+    uint4 o;
+    const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+    o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
+    o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
+    o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
+    o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
+    const int atom = cn >> 3, ch = cn & 7;
+    *reinterpret_cast<uint4*>(bst + atom * 8192 + (k >> 3) * 1024 + (k & 7) * 128 +
+                              ((ch ^ (k & 7)) << 4)) = o;
+  }
+}
+
+__device__ __forceinline__ uint4 q4_chunk(uint32_t nib, float d, float m) {
+  // nib holds 8 codes, element 2b in the low nibble of byte b, 2b+1 in the high nibble.
+  uint4 o;
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) v[e] = d * (float)((nib >> (4 * e)) & 0xFu) - m;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  return o;
+}
+
+// Q4_K, K-major output; raw [BN][32] bytes, sc [2][BN] float2 (d*sc, dmin*m).
+template <int BN>
+__device__ __forceinline__ void dequant_q4_nt(const uint8_t* raw, const float2* sc, uint8_t* bst,
+                                              int tid) {
+#pragma unroll
+  for (int j = 0; j < BN / 16; ++j) {
+    const int idx = tid + 128 * j;
+    const int r = idx >> 3, c = idx & 7;
+    const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
+    const float2 s = sc[(c >> 2) * BN + r];
+    *reinterpret_cast<uint4*>(bst + r * 128 + ((c ^ (r & 7)) << 4)) = q4_chunk(nib, s.x, s.y);
+  }
+}
+
+// Q4_K, MN-major output; raw [64][BN/2] bytes, sc [BN/32][64] float2.
+template <int BN>
+__device__ __forceinline__ void dequant_q4_tn(const uint8_t* raw, const float2* sc, uint8_t* bst,
+                                              int tid) {
+  constexpr int CPR = BN / 8;
+#pragma unroll
+  for (int j = 0; j < BN / 16; ++j) {
+    const int idx = tid + 128 * j;
+    const int k = idx / CPR, cn = idx % CPR;
+    const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + k * (BN / 2) + cn * 4);
+    const float2 s = sc[(cn >> 2) * 64 + k];
+    const int atom = cn >> 3, ch = cn & 7;
+    *reinterpret_cast<uint4*>(bst + atom * 8192 + (k >> 3) * 1024 + (k & 7) * 128 +
+                              ((ch ^ (k & 7)) << 4)) = q4_chunk(nib, s.x, s.y);
+  }
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int BN, int STAGES, int BMODE, bool A_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const __grid_constant__ CUtensorMap tm_bs, const __grid_constant__ CUtensorMap tm_ea,
+                   const __grid_constant__ CUtensorMap tm_eb, const GemmArgs args) {
+  using T = BModeTraits<BMODE>;
+  using L = GemmSmem<BN, STAGES, BMODE>;
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
+  static_assert(!T::mn || BN % 64 == 0, "MN-major B tiles are built from 64-wide atoms");
+  static_assert(!T::quant || BN >= 32, "dequant split assumes BN >= 32");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* bready = empty + STAGES;
+  uint64_t* accum = bready + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  const int nkb = (args.K + kBK - 1) / kBK;   // a ragged last block reads TMA zero fill
+  const int total = nkb + (args.has_ext ? 1 : 0);
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&bready[s], 128);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t taddr = *tmem_slot;
+
+  auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
+    if (*abort_flag) return false;
+    const uint32_t a = smem_u32(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+      if (mbar_try_wait(a, parity)) return true;
+      if ((i & 63u) == 0) {
+        if (*abort_flag) return false;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          record_error(args.err, code);
+          *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      for (int it = 0; it < total; ++it) {
+        const int s = it % STAGES;
+        const uint32_t use = (uint32_t)(it / STAGES);
+        if (it >= STAGES && !wait(&empty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) break;
+        uint8_t* a_st = smem + L::OFF_A + s * L::A_BYTES;
+        uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
+        if (it < nkb) {
+          const int k0 = it * kBK;
+          const uint32_t bbytes = T::quant ? (uint32_t)(L::RAW_BYTES + L::SC_BYTES) : (uint32_t)L::B_BYTES;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)L::A_BYTES + bbytes);
+          if (A_MN) {
+            tma_load_2d(a_st, &tm_a, &full[s], m0, k0);
+            tma_load_2d(a_st + 8192, &tm_a, &full[s], m0 + 64, k0);
+          } else {
+            tma_load_2d(a_st, &tm_a, &full[s], k0, m0);
+          }
+          uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
+          uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
+          if (BMODE == 0) {
+            tma_load_2d(b_st, &tm_b, &full[s], k0, n0);
+          } else if (BMODE == 1) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_st + j * 8192, &tm_b, &full[s], n0 + 64 * j, k0);
+          } else if (BMODE == 2) {
+            tma_load_2d(raw, &tm_b, &full[s], k0, n0);
+            tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
+          } else if (BMODE == 3) {
+            tma_load_2d(raw, &tm_b, &full[s], n0, k0);
+            tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
+          } else if (BMODE == 4) {
+            tma_load_2d(raw, &tm_b, &full[s], k0 / 2, n0);
+            tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
+          } else {
+            tma_load_2d(raw, &tm_b, &full[s], n0 / 2, k0);
+            tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
+          }
+        } else {
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(L::A_BYTES + L::B_BYTES));
+          tma_load_2d(a_st, &tm_ea, &full[s], 0, m0);
+          tma_load_2d(b_st, &tm_eb, &full[s], 0, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
+      const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
+      bool ok = true;
+      for (int it = 0; it < total && ok; ++it) {
+        const int s = it % STAGES;
+        const uint32_t use = (uint32_t)(it / STAGES);
+        if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
+        if (T::quant && it < nkb && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
+        const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
+        if (it < nkb) {
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = A_MN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
+                                     : make_sdesc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = T::mn ? make_sdesc(b_addr + kk * 2048, 8192, 1024)
+                                      : make_sdesc(b_addr + kk * 32, 16, 1024);
+            umma_bf16(taddr, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
+          }
+        } else {
+          umma_bf16(taddr, make_sdesc(a_addr, 16, 1024), make_sdesc(b_addr, 16, 1024), idesc_ext,
+                    total > 1 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      if (ok) umma_commit(accum);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant, then epilogue
+    const int tid = threadIdx.x - 64;
+    if (T::quant) {
+      for (int it = 0; it < nkb; ++it) {
+        const int s = it % STAGES;
+        const uint32_t use = (uint32_t)(it / STAGES);
+        if (!wait(&full[s], use & 1u, kErrTimeoutFull)) break;
+        const uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
+        const uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
+        uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
+        if (BMODE == 2) dequant_q8_nt<BN>(raw, reinterpret_cast<const float*>(sc), b_st, tid);
+        if (BMODE == 3) dequant_q8_tn<BN>(raw, reinterpret_cast<const float*>(sc), b_st, tid);
+        if (BMODE == 4) dequant_q4_nt<BN>(raw, reinterpret_cast<const float2*>(sc), b_st, tid);
+        if (BMODE == 5) dequant_q4_tn<BN>(raw, reinterpret_cast<const float2*>(sc), b_st, tid);
+        fence_proxy_async_smem();
+        mbar_arrive(&bready[s]);
+      }
+    }
+    const bool have = wait(accum, 0, kErrTimeoutAccum);
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = m0 + 32 * q + lane;
+    const bool row_ok = have && row < args.M;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
+      tmem_ld_wait();
+      const int nb = n0 + c0;
+      if (!row_ok || nb >= args.N) continue;
+      float f[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = nb + j;
+        float x = __uint_as_float(v[j]) * args.alpha;
+        if (n < args.N) {
+          if (args.col_scale) x *= __ldg(args.col_scale + n);
+          if (args.col_bias) x += __ldg(args.col_bias + n);
+        }
+        f[j] = x;
+      }
+      const bool full16 = nb + 16 <= args.N;
+      if (args.out) {
+        if (!args.out_trans) {
+          float* dst = args.out + (long)row * args.ldo + nb;
+          if (full16 && (args.ldo % 4 == 0)) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+              if (args.accumulate) {
+                const float4 p = *reinterpret_cast<const float4*>(dst + j);
+                o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+              }
+              *reinterpret_cast<float4*>(dst + j) = o;
+            }
+          } else {
+            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = args.accumulate ? dst[j] + f[j] : f[j];
+          }
+        } else {
+          for (int j = 0; j < 16 && nb + j < args.N; ++j) {
+            float* dst = args.out + (long)(nb + j) * args.ldo + row;
+            *dst = args.accumulate ? *dst + f[j] : f[j];
+          }
+        }
+      }
+      if (args.out_bf) {
+        if (!args.out_bf_trans) {
+          __nv_bfloat16* dst = args.out_bf + (long)row * args.ldo_bf + nb;
+          if (full16 && (args.ldo_bf % 8 == 0)) {
+            uint4 o0, o1;
+            o0.x = pack_bf16x2(f[0], f[1]);   o0.y = pack_bf16x2(f[2], f[3]);
+            o0.z = pack_bf16x2(f[4], f[5]);   o0.w = pack_bf16x2(f[6], f[7]);
+            o1.x = pack_bf16x2(f[8], f[9]);   o1.y = pack_bf16x2(f[10], f[11]);
+            o1.z = pack_bf16x2(f[12], f[13]); o1.w = pack_bf16x2(f[14], f[15]);
+            *reinterpret_cast<uint4*>(dst) = o0;
+            *reinterpret_cast<uint4*>(dst + 8) = o1;
+          } else {
+            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __float2bfloat16_rn(f[j]);
+          }
+        } else {
+          for (int j = 0; j < 16 && nb + j < args.N; ++j)
+            args.out_bf[(long)(nb + j) * args.ldo_bf + row] = __float2bfloat16_rn(f[j]);
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(taddr, L::TMEM_COLS);
+  }
+}
+
+}  // namespace sa3k

@@ -1,0 +1,271 @@
+// lora.cu -- the small, memory-bound kernels around the adapter GEMMs of dit_lin.
+//
+// dit_lin (src/dit.h:92-149) with a functional LoRA / DoRA-rows adapter computes
+//   z = x W^T + s (x A^T) B^T,   y = g * z + bias,   g = m / sqrt(nsq),
+//   nsq = bns + 2 s t2 + s^2 t3,  t2 = rowsum((W A^T) * B),  t3 = rowsum((B A A^T) * B)
+// and ggml differentiates it (src/train_ckpt.h:400).  The contractions run on the tcgen05 GEMM
+// engine; these kernels do the rank-16 bookkeeping in between: operand packing to bf16, A A^T,
+// the DoRA norm, the backward prologue dz = g * dy with dg = colsum(dy * z), and the DoRA
+// backward terms for dA, dB and dm.  Ranks up to 16 are padded to 16 (zero rows / columns).
+#include "sa3k_common.cuh"
+#include "sa3k_internal.h"
+#include "lora_kernels.h"
+
+namespace sa3k {
+
+constexpr int R = 16;   // padded rank
+
+__global__ void cvt_bf16_kernel(const float* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
+  const int64_t n4 = n / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(src)[i];
+    uint2 o;
+    o.x = pack_bf16x2(v.x, v.y);
+    o.y = pack_bf16x2(v.z, v.w);
+    reinterpret_cast<uint2*>(dst)[i] = o;
+  }
+  for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = __float2bfloat16_rn(src[i]);
+}
+
+// in f32 [rows][16] -> ext bf16 [rows][64] (mul * in in columns 0..15, zeros after) and, if
+// trans is non-null, bf16 [16][ld_trans] with trans[r][row] = mul_t * in[row][r].
+__global__ void pack_rank_kernel(const float* __restrict__ in, int rows, float mul,
+                                 __nv_bfloat16* __restrict__ ext, float mul_t,
+                                 __nv_bfloat16* __restrict__ trans, int ld_trans) {
+  const int row = blockIdx.x * blockDim.y + threadIdx.y;
+  if (row >= rows) return;
+  const int l = threadIdx.x;   // 0..31: two output columns each
+  if (ext) {
+    float a = 0.f, b = 0.f;
+    if (l < 8) {
+      a = mul * in[row * R + 2 * l];
+      b = mul * in[row * R + 2 * l + 1];
+    }
+    reinterpret_cast<uint32_t*>(ext + (int64_t)row * 64)[l] = pack_bf16x2(a, b);
+  }
+  if (trans && l < R) trans[(int64_t)l * ld_trans + row] = __float2bfloat16_rn(mul_t * in[row * R + l]);
+}
+
+// Adapter operand forms.  A f32 [rank][in], B f32 [out][rank].
+//   a_bf  bf16 [16][in]    (rows >= rank zero)      B operand of u = x A^T, A operand of W A^T
+//   at_x  bf16 [in][64]    A^T in columns 0..15     K-extension B operand of dx
+//   b_x   bf16 [out][64]   B in columns 0..15       K-extension B operand of y
+//   bt_bf bf16 [16][out]   B^T                      B operand of du = dz B
+__global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __restrict__ B, int rank,
+                                    int64_t in, int64_t out, __nv_bfloat16* __restrict__ a_bf,
+                                    __nv_bfloat16* __restrict__ at_x, __nv_bfloat16* __restrict__ b_x,
+                                    __nv_bfloat16* __restrict__ bt_bf) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (int64_t k = t0; k < in * 64; k += stride) {
+    const int64_t i = k / 64;
+    const int c = (int)(k % 64);
+    const float a = (c < rank) ? A[(int64_t)c * in + i] : 0.f;
+    at_x[k] = __float2bfloat16_rn(a);
+    if (c < R) a_bf[(int64_t)c * in + i] = __float2bfloat16_rn(a);
+  }
+  for (int64_t k = t0; k < out * 64; k += stride) {
+    const int64_t o = k / 64;
+    const int c = (int)(k % 64);
+    const float b = (c < rank) ? B[o * rank + c] : 0.f;
+    b_x[k] = __float2bfloat16_rn(b);
+    if (c < R) bt_bf[(int64_t)c * out + o] = __float2bfloat16_rn(b);
+  }
+}
+
+// AAt[r1][r2] = sum_i A[r1][i] A[r2][i] (f32 accumulate), one block of 256 threads.
+__global__ void aat_kernel(const float* __restrict__ A, int rank, int64_t in, float* __restrict__ aat) {
+  const int r1 = threadIdx.x / R, r2 = threadIdx.x % R;
+  float s = 0.f;
+  if (r1 < rank && r2 < rank)
+    for (int64_t i = 0; i < in; ++i) s = fmaf(A[r1 * in + i], A[r2 * in + i], s);
+  aat[threadIdx.x] = s;
+}
+
+// DoRA-rows norm per output row o (src/dit.h:126-144):
+//   t2 = sum_r P[o][r] B[o][r]   (P = W A^T, given transposed as pt[16][out])
+//   t3 = sum_r (B AAt)[o][r] B[o][r]
+//   nsq = bns + 2 s t2 + s^2 t3 ;  g = m / sqrt(nsq)
+__global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __restrict__ B, int rank,
+                                 int64_t out, const float* __restrict__ aat, const float* __restrict__ bns,
+                                 const float* __restrict__ m, float s, float* __restrict__ nsq,
+                                 float* __restrict__ g) {
+  __shared__ float saat[R * R];
+  saat[threadIdx.x % (R * R)] = aat[threadIdx.x % (R * R)];
+  __syncthreads();
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= out) return;
+  float b[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) b[r] = r < rank ? B[o * rank + r] : 0.f;
+  float t2 = 0.f, t3 = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    t2 = fmaf(pt[(int64_t)r * out + o], b[r], t2);
+    float bar = 0.f;
+#pragma unroll
+    for (int k = 0; k < R; ++k) bar = fmaf(b[k], saat[k * R + r], bar);
+    t3 = fmaf(bar, b[r], t3);
+  }
+  const float n2 = bns[o] + 2.f * s * t2 + s * s * t3;
+  nsq[o] = n2;
+  g[o] = m[o] / sqrtf(n2);
+}
+
+// Backward prologue over dy[S][out] (one thread per column, TOK rows per block):
+//   dz = bf16(g * dy) ;  dg[o] += sum_t dy[t][o] * (y[t][o] - bias[o]) / g[o]   (dora only)
+// With g == null this is the plain f32 -> bf16 conversion of dy.
+constexpr int kProTok = 32;
+__global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* __restrict__ y,
+                                    const float* __restrict__ bias, const float* __restrict__ g,
+                                    int64_t S, int64_t out, __nv_bfloat16* __restrict__ dz,
+                                    float* __restrict__ dg) {
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= out) return;
+  const int64_t t0 = (int64_t)blockIdx.y * kProTok;
+  const int64_t t1 = t0 + kProTok < S ? t0 + kProTok : S;
+  if (!g) {
+    for (int64_t t = t0; t < t1; ++t) dz[t * out + o] = __float2bfloat16_rn(dy[t * out + o]);
+    return;
+  }
+  const float go = g[o], bo = bias ? bias[o] : 0.f, inv = 1.f / go;
+  float acc = 0.f;
+  for (int64_t t = t0; t < t1; ++t) {
+    const float d = dy[t * out + o];
+    dz[t * out + o] = __float2bfloat16_rn(d * go);
+    acc = fmaf(d, (y[t * out + o] - bo) * inv, acc);
+  }
+  atomicAdd(dg + o, acc);
+}
+
+// DoRA backward per output row o (the derivative of the norm expression above):
+//   dm  = dg / sqrt(nsq)                      dnsq = -0.5 dg g / nsq
+//   dt2 = 2 s dnsq, dt3 = s^2 dnsq
+//   dB[o][r] += dt2 P[o][r] + 2 dt3 (B AAt)[o][r]
+//   cb[r][o] = bf16(dt2 B[o][r])   (A operand of dA += cb W, a rank-16 quant GEMM)
+//   c3[r][k] += dt3 B[o][r] B[o][k]           (dA += 2 c3 A afterwards)
+__global__ void dora_bwd_kernel(const float* __restrict__ pt, const float* __restrict__ B, int rank,
+                                int64_t out, const float* __restrict__ aat, const float* __restrict__ nsq,
+                                const float* __restrict__ g, const float* __restrict__ dg, float s,
+                                float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB,
+                                __nv_bfloat16* __restrict__ cb, float* __restrict__ c3) {
+  __shared__ float saat[R * R];
+  __shared__ float sc3[R * R];
+  saat[threadIdx.x % (R * R)] = aat[threadIdx.x % (R * R)];
+  sc3[threadIdx.x % (R * R)] = 0.f;
+  __syncthreads();
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float b[R];
+  float dt3 = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) b[r] = 0.f;
+  if (o < out) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) b[r] = r < rank ? B[o * rank + r] : 0.f;
+    const float n2 = nsq[o], d = dg[o];
+    const float dmo = d / sqrtf(n2);
+    if (dm) dm[o] = dm_accumulate ? dm[o] + dmo : dmo;
+    const float dn = -0.5f * d * g[o] / n2;
+    const float dt2 = 2.f * s * dn;
+    dt3 = s * s * dn;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      float bar = 0.f;
+#pragma unroll
+      for (int k = 0; k < R; ++k) bar = fmaf(b[k], saat[k * R + r], bar);
+      if (r < rank) dB[o * rank + r] += dt2 * pt[(int64_t)r * out + o] + 2.f * dt3 * bar;
+      cb[(int64_t)r * out + o] = __float2bfloat16_rn(dt2 * b[r]);
+    }
+  }
+  // c3 = B^T diag(dt3) B over this block's rows: warp sums, then one shared atomic per warp
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int r = 0; r < rank; ++r) {
+#pragma unroll 1
+    for (int k = r; k < rank; ++k) {
+      const float v = warp_sum(dt3 * b[r] * b[k]);
+      if (lane == 0) {
+        atomicAdd(&sc3[r * R + k], v);
+        if (k != r) atomicAdd(&sc3[k * R + r], v);
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < R * R && sc3[threadIdx.x] != 0.f) atomicAdd(c3 + threadIdx.x, sc3[threadIdx.x]);
+}
+
+// dA[r][i] += 2 sum_k c3[r][k] A[k][i]
+__global__ void dora_da_c3_kernel(const float* __restrict__ c3, const float* __restrict__ A, int rank,
+                                  int64_t in, float* __restrict__ dA) {
+  __shared__ float s3[R * R];
+  if (threadIdx.x < R * R) s3[threadIdx.x] = c3[threadIdx.x];
+  __syncthreads();
+  const int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (k >= (int64_t)rank * in) return;
+  const int r = (int)(k / in);
+  const int64_t i = k % in;
+  float acc = 0.f;
+  for (int q = 0; q < rank; ++q) acc = fmaf(s3[r * R + q], A[(int64_t)q * in + i], acc);
+  dA[k] += 2.f * acc;
+}
+
+// ----------------------------------------------------------------------------- launchers
+static unsigned grid1d(int64_t n, int threads, int cap = 148 * 16) {
+  int64_t b = (n + threads - 1) / threads;
+  if (b > cap) b = cap;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err) {
+  cvt_bf16_kernel<<<grid1d(n / 4 + 1, 256), 256, 0, c->stream>>>(src, n, dst);
+  return check_launch("cvt_bf16", err);
+}
+
+int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
+                __nv_bfloat16* trans, int ld_trans, std::string& err) {
+  dim3 blk(32, 8);
+  pack_rank_kernel<<<(unsigned)((rows + 7) / 8), blk, 0, c->stream>>>(in, rows, mul, ext, mul_t, trans, ld_trans);
+  return check_launch("pack_rank", err);
+}
+
+int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
+                   __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
+                   std::string& err) {
+  prep_adapter_kernel<<<grid1d((in + out) * 64, 256), 256, 0, c->stream>>>(A, B, rank, in, out, a_bf, at_x, b_x, bt_bf);
+  return check_launch("prep_adapter", err);
+}
+
+int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err) {
+  aat_kernel<<<1, 256, 0, c->stream>>>(A, rank, in, aat);
+  return check_launch("aat", err);
+}
+
+int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
+                const float* bns, const float* m, float s, float* nsq, float* g, std::string& err) {
+  dora_norm_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, bns, m, s, nsq, g);
+  return check_launch("dora_norm", err);
+}
+
+int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
+                   int64_t out, __nv_bfloat16* dz, float* dg, std::string& err) {
+  dim3 grid((unsigned)((out + 255) / 256), (unsigned)((S + kProTok - 1) / kProTok));
+  bwd_prologue_kernel<<<grid, 256, 0, c->stream>>>(dy, y, bias, g, S, out, dz, dg);
+  return check_launch("bwd_prologue", err);
+}
+
+int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
+               const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
+               float* dB, __nv_bfloat16* cb, float* c3, std::string& err) {
+  dora_bwd_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, nsq, g, dg, s, dm,
+                                                                       dm_acc, dB, cb, c3);
+  return check_launch("dora_bwd", err);
+}
+
+int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err) {
+  dora_da_c3_kernel<<<(unsigned)(((int64_t)rank * in + 255) / 256), 256, 0, c->stream>>>(c3, A, rank, in, dA);
+  return check_launch("dora_da_c3", err);
+}
+
+}  // namespace sa3k

@@ -1,0 +1,31 @@
+// lora_kernels.h -- launchers of the small kernels in lora.cu and adamw.cu.
+#pragma once
+
+#include "sa3k_internal.h"
+
+namespace sa3k {
+
+int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err);
+int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
+                __nv_bfloat16* trans, int ld_trans, std::string& err);
+int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
+                   __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
+                   std::string& err);
+int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err);
+int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
+                const float* bns, const float* m, float s, float* nsq, float* g, std::string& err);
+int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
+                   int64_t out, __nv_bfloat16* dz, float* dg, std::string& err);
+int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
+               const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
+               float* dB, __nv_bfloat16* cb, float* c3, std::string& err);
+int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err);
+
+// adamw.cu
+int k_sumsq(Ctx* c, const float* g, int64_t n, float inv, double* acc, std::string& err);
+int k_clip_scale(Ctx* c, const double* sumsq, float grad_clip, float inv_count, float* scales,
+                 double* norm_out, std::string& err);
+int k_adamw(Ctx* c, float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
+            float eps, float wd, float b1c, float b2c, const float* scales, std::string& err);
+
+}  // namespace sa3k

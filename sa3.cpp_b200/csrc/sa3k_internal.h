@@ -1,0 +1,109 @@
+// sa3k_internal.h -- types shared by the sa3k translation units (not part of the C ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+namespace sa3k {
+
+// ggml type ids (ggml.h enum ggml_type) for the formats the path accepts.
+enum : int { kTypeF32 = 0, kTypeF16 = 1, kTypeQ8_0 = 8, kTypeQ4_K = 12 };
+
+struct Ctx;
+
+// A frozen base weight W[out][in] in device memory (see quant.cu for the layouts).
+struct Weight {
+  int type = kTypeF32;
+  int64_t in = 0, out = 0;
+  void* raw = nullptr;               // F16/F32: the original values (dequant probe, row norms)
+  int8_t* codes = nullptr;           // Q8_0 int8 [out][in] | Q4_K nibble pairs [out][in/2]
+  float* scales = nullptr;           // Q8_0 f32 [in/32][out] | Q4_K float2 [in/32][out]
+  __nv_bfloat16* bf16 = nullptr;     // F16/F32: bf16 [out][in] operand copy
+  Ctx* owner = nullptr;
+};
+
+// Growable device scratch owned by a context.
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+
+struct Ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int* d_err = nullptr;              // device error word written by bounded waits
+  std::vector<Scratch> scratch;      // indexed by the slot enums of the callers
+  size_t sm_count = 148;
+};
+
+// Run-time lookup of the driver entry point (the library does not link libcuda, so it loads on
+// machines without a GPU driver; every call then fails with a clear error instead).
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled encode_tiled_fn(std::string& err);
+
+inline int check_launch(const char* what, std::string& err) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    err = std::string(what) + ": " + cudaGetErrorString(e);
+    return 1;
+  }
+  return 0;
+}
+
+// Scratch slot `slot` of at least `bytes` (grows; contents are not preserved on growth).
+void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
+
+int weight_repack(Ctx* c, Weight* w, std::string& err);
+int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err);
+int weight_row_norms(Ctx* c, const Weight* w, float eps, float* nsq, float* nrm, std::string& err);
+
+// ----------------------------------------------------------------------------- GEMM engine
+// B operand sources.
+enum BSource : int {
+  kB_BF16_KMAJOR = 0,   // bf16 [N][K]
+  kB_BF16_MNMAJOR = 1,  // bf16 [K][N]
+  kB_WEIGHT_NT = 2,     // weight W[out = N][in = K]           (y = x W^T)
+  kB_WEIGHT_TN = 3,     // weight W[out = K][in = N], used as W^T (dx = dy W)
+};
+
+struct GemmDesc {
+  int M = 0, N = 0, K = 0;
+  // A: bf16, K-major [M][lda] or (a_mn) MN-major [K][lda]
+  const __nv_bfloat16* a = nullptr;
+  long lda = 0;
+  int a_mn = 0;
+  // B
+  int bsrc = kB_BF16_KMAJOR;
+  const __nv_bfloat16* b = nullptr;
+  long ldb = 0;
+  const Weight* w = nullptr;
+  // K = 16 extension: ext_a bf16 [M][64], ext_b bf16 [N][64] (columns 16..63 are not read)
+  const __nv_bfloat16* ext_a = nullptr;
+  const __nv_bfloat16* ext_b = nullptr;
+  // epilogue
+  const float* col_scale = nullptr;
+  const float* col_bias = nullptr;
+  float alpha = 1.0f;
+  float* out = nullptr;
+  long ldo = 0;
+  int out_trans = 0;
+  int accumulate = 0;
+  __nv_bfloat16* out_bf = nullptr;
+  long ldo_bf = 0;
+  int out_bf_trans = 0;
+  int bn = 128;         // N tile (16, 128)
+};
+
+int gemm(Ctx* c, const GemmDesc& d, std::string& err);
+
+}  // namespace sa3k

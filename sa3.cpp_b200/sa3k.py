@@ -1,0 +1,197 @@
+"""ctypes binding of libsa3k.so (include/sa3k.h) for tests, the benchmark and Python callers.
+
+Device buffers are torch CUDA tensors (torch is only the allocator and stream here: every
+computation runs in libsa3k's own kernels).  The library must have been built in-tree
+(`python sa3.cpp_b200/build.py`); a missing library raises, there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libsa3k.so")
+
+TYPE_IDS = {"f32": 0, "f16": 1, "q8_0": 8, "q4_k": 12}
+
+# every symbol include/sa3k.h declares
+ABI_SYMBOLS = (
+    "sa3k_version", "sa3k_ctx_create", "sa3k_ctx_destroy", "sa3k_ctx_set_stream", "sa3k_sync",
+    "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_linear_fwd",
+    "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
+    "sa3k_average_clip_adamw",
+)
+
+
+class Sa3kError(RuntimeError):
+    pass
+
+
+class Adapter(ctypes.Structure):
+    _fields_ = [("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("magnitude", ctypes.c_void_p),
+                ("base_norm_sq", ctypes.c_void_p), ("scale", ctypes.c_float), ("rank", ctypes.c_int)]
+
+
+class AdamWParams(ctypes.Structure):
+    _fields_ = [("learning_rate", ctypes.c_float), ("beta1", ctypes.c_float), ("beta2", ctypes.c_float),
+                ("eps", ctypes.c_float), ("weight_decay", ctypes.c_float), ("grad_clip", ctypes.c_float)]
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise Sa3kError(f"{LIB_PATH} is not built (python sa3.cpp_b200/build.py)")
+        L = ctypes.CDLL(LIB_PATH)
+        P, I, I64, F, E = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_char_p
+        L.sa3k_version.restype = ctypes.c_char_p
+        L.sa3k_ctx_create.argtypes = [I, ctypes.POINTER(P), E, I]
+        L.sa3k_ctx_destroy.argtypes = [P]
+        L.sa3k_ctx_destroy.restype = None
+        L.sa3k_ctx_set_stream.argtypes = [P, P, E, I]
+        L.sa3k_sync.argtypes = [P, E, I]
+        L.sa3k_weight_upload.argtypes = [P, I, P, I64, I64, ctypes.POINTER(P), E, I]
+        L.sa3k_weight_free.argtypes = [P]
+        L.sa3k_weight_free.restype = None
+        L.sa3k_dequant.argtypes = [P, P, P, E, I]
+        L.sa3k_row_norms.argtypes = [P, P, F, P, P, E, I]
+        L.sa3k_linear_fwd.argtypes = [P, P, P, P, P, I64, P, E, I]
+        L.sa3k_linear_bwd.argtypes = [P, P, P, P, P, P, P, I64, P, P, P, P, I, E, I]
+        L.sa3k_linear_fwd_bwd.argtypes = [P, P, P, P, P, P, I64, P, P, P, P, P, E, I]
+        L.sa3k_linear_fwd_bwd_host.argtypes = [P, P, P, P, P, P, I64, P, P, P, P, P, E, I]
+        L.sa3k_adamw.argtypes = [P, P, P, P, P, I64, ctypes.POINTER(AdamWParams), I, E, I]
+        L.sa3k_average_clip_adamw.argtypes = [P, P, P, P, P, I64, I, ctypes.POINTER(AdamWParams), I,
+                                              ctypes.POINTER(ctypes.c_double), E, I]
+        for name in ABI_SYMBOLS:
+            if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free"):
+                getattr(L, name).restype = I
+        _lib = L
+    return _lib
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if hasattr(t, "data_ptr"):
+        return ctypes.c_void_p(t.data_ptr())
+    if hasattr(t, "ctypes"):
+        return t.ctypes.data_as(ctypes.c_void_p)
+    return t
+
+
+def _check(rc, err):
+    if rc != 0:
+        raise Sa3kError(err.value.decode(errors="replace"))
+
+
+class Context:
+    """A sa3k context bound to one CUDA device (and, by default, torch's current stream)."""
+
+    def __init__(self, device=0, use_torch_stream=True):
+        self._h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_ctx_create(device, ctypes.byref(self._h), err, 512), err)
+        self.device = device
+        if use_torch_stream:
+            import torch
+            s = torch.cuda.current_stream(device).cuda_stream
+            self.set_stream(s)
+
+    def set_stream(self, stream_handle):
+        err = ctypes.create_string_buffer(256)
+        _check(lib().sa3k_ctx_set_stream(self._h, ctypes.c_void_p(stream_handle), err, 256), err)
+
+    def sync(self):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_sync(self._h, err, 512), err)
+
+    def close(self):
+        if self._h:
+            lib().sa3k_ctx_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -------------------------------------------------------------------- weights
+    def upload(self, raw_bytes, qtype, inn, out):
+        import numpy as np
+        raw = np.ascontiguousarray(raw_bytes)
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_weight_upload(self._h, TYPE_IDS[qtype], raw.ctypes.data_as(ctypes.c_void_p),
+                                        inn, out, ctypes.byref(h), err, 512), err)
+        return Weight(self, h, qtype, inn, out)
+
+    # -------------------------------------------------------------------- ops
+    def dequant(self, w, dst):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dequant(self._h, w._h, _ptr(dst), err, 512), err)
+
+    def row_norms(self, w, eps, nsq=None, nrm=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_row_norms(self._h, w._h, eps, _ptr(nsq), _ptr(nrm), err, 512), err)
+
+    @staticmethod
+    def adapter(A, B, scale, m=None, bns=None):
+        rank = A.shape[0]
+        return Adapter(_ptr(A), _ptr(B), _ptr(m), _ptr(bns), scale, rank)
+
+    def linear_fwd(self, w, x, y, ad=None, bias=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_fwd(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias), _ptr(x),
+                                     x.shape[0], _ptr(y), err, 512), err)
+
+    def linear_bwd(self, w, x, y, dy, dx, ad=None, bias=None, dA=None, dB=None, dm=None, accumulate=False):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_bwd(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias), _ptr(x),
+                                     _ptr(y), _ptr(dy), x.shape[0], _ptr(dx), _ptr(dA), _ptr(dB), _ptr(dm),
+                                     1 if accumulate else 0, err, 512), err)
+
+    def linear_fwd_bwd(self, w, x, dy, y, dx, ad=None, bias=None, dA=None, dB=None, dm=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_fwd_bwd(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias), _ptr(x),
+                                         _ptr(dy), x.shape[0], _ptr(y), _ptr(dx), _ptr(dA), _ptr(dB), _ptr(dm),
+                                         err, 512), err)
+
+    def linear_fwd_bwd_host(self, w, x, dy, y, dx, ad=None, bias=None, dA=None, dB=None, dm=None):
+        """All arguments are numpy float32 arrays (host memory); ad holds host pointers."""
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_fwd_bwd_host(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias),
+                                              _ptr(x), _ptr(dy), x.shape[0], _ptr(y), _ptr(dx), _ptr(dA),
+                                              _ptr(dB), _ptr(dm), err, 512), err)
+
+    def adamw(self, p, g, m, v, hp: AdamWParams, step):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_adamw(self._h, _ptr(p), _ptr(g), _ptr(m), _ptr(v), p.numel(), ctypes.byref(hp),
+                                step, err, 512), err)
+
+    def average_clip_adamw(self, p, g, m, v, count, hp: AdamWParams, step, want_norm=False):
+        err = ctypes.create_string_buffer(512)
+        norm = ctypes.c_double(0.0)
+        _check(lib().sa3k_average_clip_adamw(self._h, _ptr(p), _ptr(g), _ptr(m), _ptr(v), p.numel(), count,
+                                             ctypes.byref(hp), step, ctypes.byref(norm) if want_norm else None,
+                                             err, 512), err)
+        return norm.value if want_norm else None
+
+
+class Weight:
+    def __init__(self, ctx, h, qtype, inn, out):
+        self.ctx, self._h, self.qtype, self.inn, self.out = ctx, h, qtype, inn, out
+
+    def free(self):
+        if self._h:
+            lib().sa3k_weight_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,186 @@
+"""GPU parity of the frozen-base linear (dit_lin, src/dit.h:92-149) through the C ABI.
+
+Dequantization is checked bit for bit against the C oracle (which is pinned to gguf-py);
+forward outputs and every gradient are checked against the float64 oracle on the same
+dequantized weights with the north star's bf16-operand tolerance, rel-L2 <= 1e-2.
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2      # rel-L2, bf16 tensor-core operands with f32 accumulation
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _dev(a):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def _case(qtype, S, inn, out, rank, seed, b_std=0.05):
+    rng = np.random.default_rng(seed)
+    W = rng.normal(0, 0.02, (out, inn)).astype(np.float32)
+    raw = oracle.quantize(W, qtype)
+    Wd = oracle.dequantize(raw, qtype, out, inn)
+    A = rng.normal(0, 1 / np.sqrt(inn), (rank, inn)).astype(np.float32)
+    B = rng.normal(0, b_std, (out, rank)).astype(np.float32)
+    bns, nrm = oracle.row_norms(Wd)
+    m = (nrm * rng.uniform(0.9, 1.2, out)).astype(np.float32)
+    x = rng.normal(0, 1, (S, inn)).astype(np.float32)
+    dy = rng.normal(0, 1, (S, out)).astype(np.float32)
+    bias = rng.normal(0, 0.1, out).astype(np.float32)
+    return dict(raw=raw, Wd=Wd, A=A, B=B, bns=bns, m=m, x=x, dy=dy, bias=bias)
+
+
+@pytest.mark.parametrize("qtype,inn,out", [("q8_0", 1536, 384), ("q4_k", 512, 640),
+                                           ("f16", 320, 192), ("f32", 192, 256)])
+def test_dequant_bit_exact(ctx, qtype, inn, out):
+    import torch
+    c = _case(qtype, 4, inn, out, 2, 1)
+    w = ctx.upload(c["raw"], qtype, inn, out)
+    dst = torch.empty(out, inn, dtype=torch.float32, device="cuda")
+    ctx.dequant(w, dst)
+    ctx.sync()
+    got = dst.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), c["Wd"].view(np.uint32))
+
+
+def test_dequant_golden_q4_k_random_blocks(ctx):
+    import os
+    import torch
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "q4_k.npz"))
+    raw = g["raw_rand"]
+    out, inn = raw.shape[0], raw.shape[1] // 144 * 256
+    w = ctx.upload(raw, "q4_k", inn, out)
+    dst = torch.empty(out, inn, dtype=torch.float32, device="cuda")
+    ctx.dequant(w, dst)
+    ctx.sync()
+    assert np.array_equal(dst.cpu().numpy().view(np.uint32), g["deq_rand"].view(np.uint32))
+
+
+@pytest.mark.parametrize("qtype", ["q8_0", "q4_k"])
+def test_row_norms(ctx, qtype):
+    import torch
+    c = _case(qtype, 4, 512, 384, 2, 2)
+    w = ctx.upload(c["raw"], qtype, 512, 384)
+    nsq = torch.empty(384, device="cuda")
+    nrm = torch.empty(384, device="cuda")
+    ctx.row_norms(w, 1e-12, nsq, nrm)
+    ctx.sync()
+    ref_nsq, ref_nrm = oracle.row_norms(c["Wd"])
+    np.testing.assert_allclose(nsq.cpu().numpy(), ref_nsq, rtol=1e-6)
+    np.testing.assert_allclose(nrm.cpu().numpy(), ref_nrm, rtol=1e-6)
+
+
+def _run(ctx, qtype, mode, S, inn, out, rank, seed=3, api="fwd_bwd"):
+    import torch
+    c = _case(qtype, S, inn, out, rank, seed)
+    s = 16.0 / rank if rank == 16 else 2.0
+    w = ctx.upload(c["raw"], qtype, inn, out)
+    x, dy, bias = _dev(c["x"]), _dev(c["dy"]), _dev(c["bias"])
+    A, B, m, bns = _dev(c["A"]), _dev(c["B"]), _dev(c["m"]), _dev(c["bns"])
+    ad = None
+    if mode != "plain":
+        ad = ctx.adapter(A, B, s, m if mode == "dora" else None, bns if mode == "dora" else None)
+    y = torch.empty(S, out, device="cuda")
+    dx = torch.empty(S, inn, device="cuda")
+    dA = torch.empty(rank, inn, device="cuda")
+    dB = torch.empty(out, rank, device="cuda")
+    dm = torch.empty(out, device="cuda")
+    kw = dict(ad=ad, bias=bias, dA=dA if ad else None, dB=dB if ad else None, dm=dm if mode == "dora" else None)
+    if api == "fwd_bwd":
+        ctx.linear_fwd_bwd(w, x, dy, y, dx, **kw)
+    else:
+        ctx.linear_fwd(w, x, y, ad=ad, bias=bias)
+        ctx.linear_bwd(w, x, y, dy, dx, **kw)
+    ctx.sync()
+    ref_y, cache = oracle.dit_lin_fwd(c["x"], c["Wd"], c["A"] if ad else None, c["B"] if ad else None, s,
+                                      c["m"] if mode == "dora" else None, c["bns"] if mode == "dora" else None,
+                                      c["bias"])
+    ref = oracle.dit_lin_bwd(c["dy"], cache)
+    res = {"y": rel_l2(y.cpu().numpy(), ref_y), "dx": rel_l2(dx.cpu().numpy(), ref["dx"])}
+    if ad:
+        res["dA"] = rel_l2(dA.cpu().numpy(), ref["dA"])
+        res["dB"] = rel_l2(dB.cpu().numpy(), ref["dB"])
+    if mode == "dora":
+        res["dm"] = rel_l2(dm.cpu().numpy(), ref["dm"])
+    return res
+
+
+@pytest.mark.parametrize("qtype", ["q8_0", "q4_k", "f16", "f32"])
+@pytest.mark.parametrize("mode", ["plain", "lora", "dora"])
+def test_linear_fwd_bwd_small(ctx, qtype, mode):
+    res = _run(ctx, qtype, mode, S=200, inn=512, out=384, rank=16)
+    assert all(v < TOL for v in res.values()), res
+
+
+@pytest.mark.parametrize("rank", [2, 16])
+def test_linear_separate_fwd_then_bwd(ctx, rank):
+    res = _run(ctx, "q8_0", "dora", S=130, inn=256, out=512, rank=rank, api="separate")
+    assert all(v < TOL for v in res.values()), res
+
+
+def test_linear_config1_q8_0_lora(ctx):
+    # 1536 x 1536 Q8_0, 1024 tokens, LoRA r 16 / alpha 16
+    res = _run(ctx, "q8_0", "lora", S=1024, inn=1536, out=1536, rank=16, seed=11)
+    assert all(v < TOL for v in res.values()), res
+
+
+def test_linear_config2_q4_k_dora(ctx):
+    # 1536 -> 6144 Q4_K, 2048 tokens, DoRA r 16 / alpha 16
+    res = _run(ctx, "q4_k", "dora", S=2048, inn=1536, out=6144, rank=16, seed=12)
+    assert all(v < TOL for v in res.values()), res
+
+
+def test_linear_accumulate(ctx):
+    import torch
+    c = _case("q8_0", 96, 256, 256, 16, 5)
+    w = ctx.upload(c["raw"], "q8_0", 256, 256)
+    x, dy = _dev(c["x"]), _dev(c["dy"])
+    A, B = _dev(c["A"]), _dev(c["B"])
+    ad = ctx.adapter(A, B, 1.0)
+    y = torch.empty(96, 256, device="cuda")
+    ctx.linear_fwd(w, x, y, ad=ad)
+    dx = torch.zeros(96, 256, device="cuda")
+    dA = torch.zeros(16, 256, device="cuda")
+    dB = torch.zeros(256, 16, device="cuda")
+    for _ in range(2):
+        ctx.linear_bwd(w, x, y, dy, dx, ad=ad, dA=dA, dB=dB, accumulate=True)
+    ctx.sync()
+    _, cache = oracle.dit_lin_fwd(c["x"], c["Wd"], c["A"], c["B"], 1.0)
+    ref = oracle.dit_lin_bwd(c["dy"], cache)
+    assert rel_l2(dx.cpu().numpy(), 2 * ref["dx"]) < TOL
+    assert rel_l2(dA.cpu().numpy(), 2 * ref["dA"]) < TOL
+    assert rel_l2(dB.cpu().numpy(), 2 * ref["dB"]) < TOL
+
+
+def test_host_buffer_entry_point(ctx):
+    c = _case("q8_0", 64, 256, 128, 16, 6)
+    w = ctx.upload(c["raw"], "q8_0", 256, 128)
+    import sa3k
+    ad = sa3k.Context.adapter(c["A"], c["B"], 1.0, c["m"], c["bns"])
+    y = np.empty((64, 128), np.float32)
+    dx = np.empty((64, 256), np.float32)
+    dA = np.empty((16, 256), np.float32)
+    dB = np.empty((128, 16), np.float32)
+    dm = np.empty(128, np.float32)
+    ctx.linear_fwd_bwd_host(w, c["x"], c["dy"], y, dx, ad=ad, bias=c["bias"], dA=dA, dB=dB, dm=dm)
+    ref_y, cache = oracle.dit_lin_fwd(c["x"], c["Wd"], c["A"], c["B"], 1.0, c["m"], c["bns"], c["bias"])
+    ref = oracle.dit_lin_bwd(c["dy"], cache)
+    assert rel_l2(y, ref_y) < TOL
+    for name, got in (("dx", dx), ("dA", dA), ("dB", dB), ("dm", dm)):
+        assert rel_l2(got, ref[name]) < TOL, name
+
+
+def test_bad_arguments_raise(ctx):
+    import sa3k
+    c = _case("q8_0", 8, 256, 128, 2, 7)
+    with pytest.raises(sa3k.Sa3kError):
+        ctx.upload(c["raw"], "q4_k", 256 + 64, 128)      # Q4_K needs in % 256 == 0
