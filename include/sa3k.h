@@ -42,14 +42,43 @@ const char* sa3k_version(void);
 int sa3k_ctx_create(int device, sa3k_ctx** out, char* err, int err_len);
 void sa3k_ctx_destroy(sa3k_ctx* ctx);
 
-/* Run subsequent work on `cuda_stream` (a cudaStream_t of the context's device; NULL restores
- * the private stream).  No counterpart in the reference (ggml owns its streams). */
+/* Run subsequent work on `cuda_stream`, a cudaStream_t of the context's device (NULL is CUDA's
+ * legacy default stream).  The context's private stream is released on the first call.
+ * No counterpart in the reference (ggml owns its streams). */
 int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len);
+
+/* Context options (sa3k_ctx_set_option).  No counterpart in the reference.
+ *   SA3K_OPT_WEIGHT_BF16_CACHE  1 (default): a Q8_0 / Q4_K weight uploaded afterwards also keeps
+ *       a bf16 operand copy, made once by the bit-exact dequantizer (the frozen base never
+ *       changes, so the tensor cores then read bf16 tiles directly).  0: codes + scales only.
+ *   SA3K_OPT_SMEM_DEQUANT  1: GEMMs over quantized weights dequantize each TMA-loaded tile in
+ *       shared memory even when a bf16 copy exists.  0 (default): use the copy when present.
+ * Both paths round the same f32 dequantized value once to bf16, so results are identical. */
+#define SA3K_OPT_WEIGHT_BF16_CACHE 1
+#define SA3K_OPT_SMEM_DEQUANT 2
+int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded
  * wait that timed out inside a kernel is reported here and cleared).
  * Counterpart of the implicit sync in ggml_backend_tensor_get (src/train_loop.h:371). */
 int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len);
+
+/* Per launch-class counters of this context: every kernel launch is counted by class
+ * ("linear.fwd", "linear.dx", "lora.dA", "adamw", ...); with timing != 0 each launch is also
+ * bracketed by CUDA events on the context's stream.  Enabling (or disabling) resets the
+ * counters.  Counterpart of the SA3_TRAIN_PROFILE phase timers (src/train_loop.h:314-437). */
+typedef struct sa3k_profile_entry {
+  char name[48];
+  int64_t launches;
+  double total_ms;   /* summed event time of those launches (0 unless timing was on) */
+} sa3k_profile_entry;
+
+int sa3k_profile_enable(sa3k_ctx* ctx, int timing, char* err, int err_len);
+
+/* Copy up to `max` entries into `out` (may be NULL to count) and the number of classes into
+ * *n_out.  Synchronizes the context's stream. */
+int sa3k_profile_read(sa3k_ctx* ctx, sa3k_profile_entry* out, int max, int* n_out, char* err,
+                      int err_len);
 
 /* Upload one frozen base weight from raw GGUF row bytes (host memory), ggml type
  * F32 / F16 / Q8_0 / Q4_K, and repack it for the tensor-core engine.  `in` must be a multiple of

@@ -143,26 +143,27 @@ def row_norms(w: np.ndarray, eps: float = 1e-12):
 # --------------------------------------------------------------------------------------------
 # dit_lin: functional LoRA / DoRA-rows linear (src/dit.h:92-149), forward and backward
 # --------------------------------------------------------------------------------------------
-def dit_lin_fwd(x, W, A=None, B=None, scale=1.0, m=None, bns=None, bias=None):
-    """y[S][out].  x[S][in], W[out][in], A[r][in], B[out][r], m/bns[out].  float64.
+def dit_lin_fwd(x, W, A=None, B=None, scale=1.0, m=None, bns=None, bias=None, dtype=np.float64):
+    """y[S][out].  x[S][in], W[out][in], A[r][in], B[out][r], m/bns[out].  float64 by default
+    (dtype=np.float32 is the timed CPU-baseline variant: ggml's CPU backend computes in f32).
 
     y = g * (x W^T + s (x A^T) B^T) + bias,  g = m / sqrt(bns + 2s t2 + s^2 t3)  (dora)
     t2[o] = sum_r (W A^T)[o,r] B[o,r]          (src/dit.h:132-135)
     t3[o] = sum_r B[o,r] (B A A^T)[o,r]         (src/dit.h:136-138)
     """
-    x = np.asarray(x, np.float64)
-    W = np.asarray(W, np.float64)
+    x = np.asarray(x, dtype)
+    W = np.asarray(W, dtype)
     z = x @ W.T
-    cache = {"x": x, "W": W}
+    cache = {"x": x, "W": W, "dtype": dtype}
     if A is not None:
-        A = np.asarray(A, np.float64)
-        B = np.asarray(B, np.float64)
+        A = np.asarray(A, dtype)
+        B = np.asarray(B, dtype)
         u = x @ A.T
         z = z + scale * (u @ B.T)
         cache.update(A=A, B=B, u=u, scale=scale)
         if m is not None:
-            m = np.asarray(m, np.float64)
-            bns = np.asarray(bns, np.float64)
+            m = np.asarray(m, dtype)
+            bns = np.asarray(bns, dtype)
             P = W @ A.T
             AAt = A @ A.T
             BAAt = B @ AAt
@@ -177,13 +178,13 @@ def dit_lin_fwd(x, W, A=None, B=None, scale=1.0, m=None, bns=None, bias=None):
     else:
         y = z
     if bias is not None:
-        y = y + np.asarray(bias, np.float64)
+        y = y + np.asarray(bias, dtype)
     return y, cache
 
 
 def dit_lin_bwd(dy, cache):
     """Gradients of dit_lin for upstream dy[S][out]: dict(dx, dA, dB, dm)."""
-    dy = np.asarray(dy, np.float64)
+    dy = np.asarray(dy, cache.get("dtype", np.float64))
     x, W = cache["x"], cache["W"]
     out = {}
     if "g" in cache:

@@ -76,18 +76,21 @@ static unsigned blocks_for(int64_t n) {
 }
 
 int k_sumsq(Ctx* c, const float* g, int64_t n, float inv, double* acc, std::string& err) {
+  ProfScope prof_(c, "sumsq");
   sumsq_kernel<<<blocks_for(n), 256, 0, c->stream>>>(g, n, inv, acc);
   return check_launch("sumsq", err);
 }
 
 int k_clip_scale(Ctx* c, const double* sumsq, float grad_clip, float inv_count, float* scales,
                  double* norm_out, std::string& err) {
+  ProfScope prof_(c, "clip_scale");
   clip_scale_kernel<<<1, 1, 0, c->stream>>>(sumsq, grad_clip, inv_count, scales, norm_out);
   return check_launch("clip_scale", err);
 }
 
 int k_adamw(Ctx* c, float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
             float eps, float wd, float b1c, float b2c, const float* scales, std::string& err) {
+  ProfScope prof_(c, "adamw");
   adamw_kernel<<<blocks_for(n), 256, 0, c->stream>>>(p, g, m, v, n, lr, b1, b2, eps, wd, b1c, b2c, scales);
   return check_launch("adamw", err);
 }

@@ -127,6 +127,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.a = b.x_bf; g.lda = in;
     g.bsrc = kB_BF16_KMAJOR; g.b = b.a_bf; g.ldb = in;
     g.out = b.u; g.ldo = 16; g.bn = 16;
+    g.name = "lora.u";
     if (gemm(c, g, err)) return 1;
     if (k_pack_rank(c, b.u, (int)S, s, b.ext_u, 1.0f, bwd ? b.ut : nullptr, (int)b.s_pad, err)) return 1;
   }
@@ -137,6 +138,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.a = b.a_bf; g.lda = in;
     g.bsrc = kB_WEIGHT_NT; g.w = w;
     g.out = b.pt; g.ldo = out;
+    g.name = "dora.P";
     if (gemm(c, g, err)) return 1;
     if (k_aat(c, ad->A, rank, in, b.aat, err)) return 1;
     if (k_dora_norm(c, b.pt, ad->B, rank, out, b.aat, ad->base_norm_sq, ad->magnitude, s, b.nsq, b.g, err)) return 1;
@@ -150,6 +152,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.col_scale = dora ? b.g : nullptr;
     g.col_bias = bias;
     g.out = y_out; g.ldo = out;
+    g.name = "linear.fwd";
     if (gemm(c, g, err)) return 1;
   }
   if (!bwd) return 0;
@@ -166,6 +169,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.bsrc = kB_BF16_KMAJOR; g.b = b.bt_bf; g.ldb = out;
     g.alpha = s;
     g.out = b.du; g.ldo = 16; g.bn = 16;
+    g.name = "lora.du";
     if (gemm(c, g, err)) return 1;
     if (k_pack_rank(c, b.du, (int)S, 1.0f, b.ext_du, 1.0f, b.dut, (int)b.s_pad, err)) return 1;
   }
@@ -177,6 +181,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.bsrc = kB_WEIGHT_TN; g.w = w;
     if (adapter) { g.ext_a = b.ext_du; g.ext_b = b.at_x; }
     g.out = dx; g.ldo = in; g.accumulate = accumulate;
+    g.name = "linear.dx";
     if (gemm(c, g, err)) return 1;
   }
   if (!adapter) return 0;
@@ -188,6 +193,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.bsrc = kB_BF16_KMAJOR; g.b = b.ut; g.ldb = b.s_pad;
     g.alpha = s;
     g.out = dB; g.ldo = rank; g.accumulate = accumulate; g.bn = 16;
+    g.name = "lora.dB";
     if (gemm(c, g, err)) return 1;
   }
   {
@@ -197,6 +203,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.a = b.dut; g.lda = b.s_pad;
     g.bsrc = kB_BF16_MNMAJOR; g.b = b.x_bf; g.ldb = in;
     g.out = dA; g.ldo = in; g.accumulate = accumulate;
+    g.name = "lora.dA";
     if (gemm(c, g, err)) return 1;
   }
   if (dora) {
@@ -207,10 +214,55 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     g.a = b.cb; g.lda = out;
     g.bsrc = kB_WEIGHT_TN; g.w = w;
     g.out = dA; g.ldo = in; g.accumulate = 1;
+    g.name = "dora.dA";
     if (gemm(c, g, err)) return 1;
     if (k_dora_da_c3(c, b.c3, ad->A, rank, in, dA, err)) return 1;
   }
   return 0;
+}
+
+ProfScope::ProfScope(Ctx* ctx, const char* name) : c(ctx) {
+  for (size_t i = 0; i < c->prof.size(); ++i)
+    if (c->prof[i].name == name) { idx = (int)i; break; }
+  if (idx < 0) {
+    c->prof.push_back(ProfEntry{});
+    c->prof.back().name = name;
+    idx = (int)c->prof.size() - 1;
+  }
+  c->prof[(size_t)idx].launches += 1;
+  if (c->timing) {
+    if (c->ev_pool.empty()) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      c->ev_pool.push_back(e);
+    }
+    e0 = c->ev_pool.back();
+    c->ev_pool.pop_back();
+    cudaEventRecord(e0, c->stream);
+  }
+}
+
+ProfScope::~ProfScope() {
+  if (!e0) return;
+  cudaEvent_t e1;
+  if (c->ev_pool.empty()) cudaEventCreate(&e1);
+  else { e1 = c->ev_pool.back(); c->ev_pool.pop_back(); }
+  cudaEventRecord(e1, c->stream);
+  c->prof[(size_t)idx].pending.emplace_back(e0, e1);
+}
+
+static void prof_collect(Ctx* c) {
+  cudaStreamSynchronize(c->stream);
+  for (ProfEntry& p : c->prof) {
+    for (auto& ev : p.pending) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, ev.first, ev.second) == cudaSuccess) p.ms += ms;
+      c->ev_pool.push_back(ev.first);
+      c->ev_pool.push_back(ev.second);
+    }
+    p.pending.clear();
+  }
+  cudaGetLastError();
 }
 
 static int adamw_bias_corrections(const sa3k_adamw_params* hp, int step, float& b1c, float& b2c) {
@@ -259,7 +311,8 @@ int sa3k_ctx_create(int device, sa3k_ctx** out, char* err, int err_len) {
 void sa3k_ctx_destroy(sa3k_ctx* ctx) {
   if (!ctx) return;
   cudaSetDevice(ctx->c.device);
-  cudaStreamSynchronize(ctx->c.stream);
+  prof_collect(&ctx->c);
+  for (cudaEvent_t e : ctx->c.ev_pool) cudaEventDestroy(e);
   for (auto& s : ctx->c.scratch)
     if (s.ptr) cudaFree(s.ptr);
   if (ctx->c.d_err) cudaFree(ctx->c.d_err);
@@ -269,21 +322,23 @@ void sa3k_ctx_destroy(sa3k_ctx* ctx) {
 
 int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* stream, char* err, int err_len) {
   if (!ctx) return fill_err(err, err_len, "ctx is NULL");
-  if (!stream) {
-    if (!ctx->c.own_stream) {
-      if (cudaStreamCreateWithFlags(&ctx->c.stream, cudaStreamNonBlocking) != cudaSuccess)
-        return fill_err(err, err_len, "failed to create stream");
-      ctx->c.own_stream = true;
-    }
-    return 0;
-  }
+  cudaSetDevice(ctx->c.device);
   if (ctx->c.own_stream) {
     cudaStreamSynchronize(ctx->c.stream);
     cudaStreamDestroy(ctx->c.stream);
+    ctx->c.own_stream = false;
   }
-  ctx->c.stream = static_cast<cudaStream_t>(stream);
-  ctx->c.own_stream = false;
+  ctx->c.stream = static_cast<cudaStream_t>(stream);   // NULL is CUDA's legacy default stream
   return 0;
+}
+
+int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  switch (option) {
+    case SA3K_OPT_WEIGHT_BF16_CACHE: ctx->c.weight_cache = value != 0; return 0;
+    case SA3K_OPT_SMEM_DEQUANT: ctx->c.smem_dequant = value != 0; return 0;
+    default: return fill_err(err, err_len, "unknown option");
+  }
 }
 
 int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len) {
@@ -298,6 +353,33 @@ int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len) {
     cudaMemset(ctx->c.d_err, 0, sizeof(int));
     return fill_err(err, err_len, "device wait timed out inside a kernel (code " + std::to_string(code) + ")");
   }
+  return 0;
+}
+
+int sa3k_profile_enable(sa3k_ctx* ctx, int timing, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  cudaSetDevice(ctx->c.device);
+  prof_collect(&ctx->c);
+  ctx->c.prof.clear();
+  ctx->c.timing = timing != 0;
+  return 0;
+}
+
+int sa3k_profile_read(sa3k_ctx* ctx, sa3k_profile_entry* out, int max, int* n_out, char* err, int err_len) {
+  if (!ctx || !n_out) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  prof_collect(&ctx->c);
+  int n = 0;
+  for (const ProfEntry& p : ctx->c.prof) {
+    if (out && n < max) {
+      std::memset(out[n].name, 0, sizeof out[n].name);
+      std::strncpy(out[n].name, p.name.c_str(), sizeof out[n].name - 1);
+      out[n].launches = p.launches;
+      out[n].total_ms = p.ms;
+    }
+    ++n;
+  }
+  *n_out = n;
   return 0;
 }
 
@@ -322,7 +404,7 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
   sa3k_weight* h = new (std::nothrow) sa3k_weight();
   if (!h) return fill_err(err, err_len, "out of host memory");
   Weight& w = h->w;
-  w.type = type; w.in = in; w.out = out; w.owner = &ctx->c;
+  w.type = type; w.in = in; w.out = out; w.device = ctx->c.device;
   std::string e;
   auto fail = [&](const std::string& msg) {
     if (w.raw) cudaFree(w.raw);
@@ -348,6 +430,10 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
     if (cudaMalloc(&w.bf16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight)");
   }
   if (weight_repack(&ctx->c, &w, e)) return fail(e);
+  if ((type == kTypeQ8_0 || type == kTypeQ4_K) && ctx->c.weight_cache) {
+    if (cudaMalloc(&w.bf16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight cache)");
+    if (weight_cache_bf16(&ctx->c, &w, e)) return fail(e);
+  }
   if (cudaStreamSynchronize(ctx->c.stream) != cudaSuccess) return fail("weight repack failed");
   if (type == kTypeQ8_0 || type == kTypeQ4_K) {   // codes + scales carry every bit of the blocks
     cudaFree(w.raw);
@@ -360,10 +446,7 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
 void sa3k_weight_free(sa3k_weight* h) {
   if (!h) return;
   Weight& w = h->w;
-  if (w.owner) {
-    cudaSetDevice(w.owner->device);
-    cudaStreamSynchronize(w.owner->stream);
-  }
+  cudaSetDevice(w.device);   // cudaFree waits for the device's outstanding work
   if (w.raw) cudaFree(w.raw);
   if (w.codes) cudaFree(w.codes);
   if (w.scales) cudaFree(w.scales);

@@ -53,6 +53,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
                   const CUtensorMap& tbs, const CUtensorMap& tea, const CUtensorMap& teb,
                   const GemmArgs& args, std::string& err) {
   using L = GemmSmem<BN, STAGES, BMODE>;
+  using R = GemmRoles<BMODE>;
   auto kern = gemm_tc_kernel<BN, STAGES, BMODE, A_MN>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -60,9 +61,23 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
       return check_launch("gemm smem attribute", err);
     attr_set = true;
   }
-  dim3 grid((unsigned)((d.M + kBM - 1) / kBM), (unsigned)((d.N + BN - 1) / BN));
-  kern<<<grid, kThreads, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, args);
+  const long tiles = (long)((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
+  const unsigned grid = (unsigned)(tiles < (long)c->sm_count ? tiles : (long)c->sm_count);
+  ProfScope prof_(c, d.name);
+  kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, args);
   return check_launch("gemm_tc", err);
+}
+
+// N tile for the main GEMMs: the cheaper of 128 / 256 by a wave-quantized cost model.
+static int pick_bn(const Ctx* c, int M, int N) {
+  if (N <= 128) return 128;
+  const long tm = (M + kBM - 1) / kBM;
+  auto cost = [&](int bn) {
+    const long tiles = tm * ((N + bn - 1) / bn);
+    const long waves = (tiles + (long)c->sm_count - 1) / (long)c->sm_count;
+    return waves * (bn + 24);   // + per-tile overhead (prologue / epilogue tail)
+  };
+  return cost(256) <= cost(128) ? 256 : 128;
 }
 
 int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
@@ -70,15 +85,15 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
     err = "gemm: need M, N > 0 and K > 0";
     return 1;
   }
-  const bool quant = (d.bsrc == kB_WEIGHT_NT || d.bsrc == kB_WEIGHT_TN) && d.w &&
-                     (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K);
-  const int bn = d.bn;
-  if (!(bn == 16 || bn == 128)) {
+  const bool weight_b = d.bsrc == kB_WEIGHT_NT || d.bsrc == kB_WEIGHT_TN;
+  // quantized weights run through the in-smem dequant path unless a bf16 operand copy exists
+  // and the context has not asked for the in-smem path explicitly
+  const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
+                     !(d.w->bf16 && !c->smem_dequant);
+  int bn = d.bn;
+  if (bn == 128) bn = pick_bn(c, d.M, d.N);
+  if (!(bn == 16 || bn == 128 || bn == 256)) {
     err = "gemm: unsupported N tile";
-    return 1;
-  }
-  if (quant && bn != 128) {
-    err = "gemm: quantized B needs the 128-wide N tile";
     return 1;
   }
   CUtensorMap ta, tb, tbs, tea, teb;
@@ -108,7 +123,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       err = "gemm: weight shape does not match the GEMM";
       return 1;
     }
-    if (w->type == kTypeQ8_0) {
+    if (quant && w->type == kTypeQ8_0) {
       bmode = nt ? 2 : 3;
       const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       const auto F32 = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
@@ -119,7 +134,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
         if (make_map(&tb, U8, w->codes, w->in, w->out, w->in, bn, 64, NOSW, "Q8_0 codes", err)) return 1;
         if (make_map(&tbs, F32, w->scales, w->out, w->in / 32, w->out * 4, 64, bn / 32, NOSW, "Q8_0 scales", err)) return 1;
       }
-    } else if (w->type == kTypeQ4_K) {
+    } else if (quant && w->type == kTypeQ4_K) {
       bmode = nt ? 4 : 5;
       const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
       const auto U64 = CU_TENSOR_MAP_DATA_TYPE_UINT64;
@@ -131,7 +146,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
         if (make_map(&tbs, U64, w->scales, w->out, w->in / 32, w->out * 8, 64, bn / 32, NOSW, "Q4_K scales", err)) return 1;
       }
     } else {
-      // F16 / F32 bases run on their bf16 copy
+      // F16 / F32 bases, and quantized bases with a dequantized cache, run on the bf16 copy
       if (nt) {
         bmode = 0;
         if (make_map(&tb, BF, w->bf16, w->in, w->out, w->in * 2, 64, bn, SW, "W bf16", err)) return 1;
@@ -164,9 +179,19 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
                   : launch<16, 8, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
   }
   if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
+  if (bn == 256) {
+    switch (bmode) {
+      case 0: return launch<256, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+      case 1: return launch<256, 4, 1, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+      case 2: return launch<256, 3, 2, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+      case 3: return launch<256, 3, 3, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+      case 4: return launch<256, 3, 4, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+      default: return launch<256, 3, 5, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    }
+  }
   switch (bmode) {
-    case 0: return launch<128, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
-    case 1: return launch<128, 4, 1, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 0: return launch<128, 6, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    case 1: return launch<128, 6, 1, false>(c, d, ta, tb, tbs, tea, teb, a, err);
     case 2: return launch<128, 4, 2, false>(c, d, ta, tb, tbs, tea, teb, a, err);
     case 3: return launch<128, 4, 3, false>(c, d, ta, tb, tbs, tea, teb, a, err);
     case 4: return launch<128, 4, 4, false>(c, d, ta, tb, tbs, tea, teb, a, err);

@@ -50,7 +50,6 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128, kBK = 64;
-constexpr int kThreads = 192;
 
 template <int BMODE>
 struct BModeTraits {
@@ -61,6 +60,15 @@ struct BModeTraits {
 };
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
+
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 epilogue, 6.. dequant (quant only).
+template <int BMODE>
+struct GemmRoles {
+  static constexpr int EPI_WARPS = 4;
+  static constexpr int DQ_WARPS = BModeTraits<BMODE>::quant ? 8 : 0;
+  static constexpr int THREADS = 32 * (2 + EPI_WARPS + DQ_WARPS);
+  static constexpr int DQ_THREADS = 32 * DQ_WARPS;
+};
 
 template <int BN, int STAGES, int BMODE>
 struct GemmSmem {
@@ -77,60 +85,33 @@ struct GemmSmem {
   static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_STRIDE;
   static constexpr int OFF_BAR = align_up(OFF_SC + STAGES * SC_STRIDE, 64);
-  static constexpr int BAR_BYTES = (3 * STAGES + 1) * 8 + 16;
+  static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
   static constexpr int DYN = TOTAL + 1024;   // slack for 1024-byte alignment of the base
-  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int ACC_COLS = BN < 32 ? 32 : BN;           // one accumulator buffer
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;               // double-buffered
+  static_assert(TMEM_COLS == 64 || TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128,
+                "TMEM allocation must be a power of two >= 32");
+  static_assert(DYN <= 232448, "shared memory budget (227 KB)");
 };
 
 // ------------------------------------------------------------------ dequantization stages
-// Each of the 128 dequant threads writes BN/16 16-byte chunks (8 bf16) of the B stage.
+// NT threads of the dequant warps each write BN*8/NT 16-byte chunks (8 bf16) of the B stage.
 
-// Q8_0, K-major output [BN rows = out][64 k = in]; raw [BN][64] int8, sc [2][BN] f32.
-template <int BN>
-__device__ __forceinline__ void dequant_q8_nt(const uint8_t* raw, const float* sc, uint8_t* bst,
-                                              int tid) {
-#pragma unroll
-  for (int j = 0; j < BN / 16; ++j) {
-    const int idx = tid + 128 * j;
-    const int r = idx >> 3, c = idx & 7;
-    const uint2 q = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);
-    const float s = sc[(c >> 2) * BN + r];
-    uint4 o;
-    const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
-    o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
-    o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
-    o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
-    o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
-    *reinterpret_cast<uint4*>(bst + r * 128 + ((c ^ (r & 7)) << 4)) = o;
-  }
-}
-
-// Q8_0, MN-major output [64 k = out][BN n = in]; raw [64][BN] int8, sc [BN/32][64] f32.
-template <int BN>
-__device__ __forceinline__ void dequant_q8_tn(const uint8_t* raw, const float* sc, uint8_t* bst,
-                                              int tid) {
-  constexpr int CPR = BN / 8;   // chunks per k-row
-#pragma unroll
-  for (int j = 0; j < BN / 16; ++j) {
-    const int idx = tid + 128 * j;
-    const int k = idx / CPR, cn = idx % CPR;
-    const uint2 q = *reinterpret_cast<const uint2*>(raw + k * BN + cn * 8);
-    const float s = sc[(cn >> 2) * 64 + k];
-    uint4 o;
-    const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
-    o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
-    o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
-    o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
-    o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
-    const int atom = cn >> 3, ch = cn & 7;
-    *reinterpret_cast<uint4*>(bst + atom * 8192 + (k >> 3) * 1024 + (k & 7) * 128 +
-                              ((ch ^ (k & 7)) << 4)) = o;
-  }
+__device__ __forceinline__ uint4 q8_chunk(uint2 q, float s) {
+  uint4 o;
+  const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
+  o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
+  o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
+  o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
+  o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
+  return o;
 }
 
 __device__ __forceinline__ uint4 q4_chunk(uint32_t nib, float d, float m) {
-  // nib holds 8 codes, element 2b in the low nibble of byte b, 2b+1 in the high nibble.
+  // nib holds 8 codes, element 2b in the low nibble of byte b, 2b+1 in the high nibble;
+  // d*q is exact in f32 (<= 21 significant bits), so the FMA below rounds exactly like ggml's
+  // separate multiply and subtract.
   uint4 o;
   float v[8];
 #pragma unroll
@@ -142,48 +123,61 @@ __device__ __forceinline__ uint4 q4_chunk(uint32_t nib, float d, float m) {
   return o;
 }
 
-// Q4_K, K-major output; raw [BN][32] bytes, sc [2][BN] float2 (d*sc, dmin*m).
-template <int BN>
-__device__ __forceinline__ void dequant_q4_nt(const uint8_t* raw, const float2* sc, uint8_t* bst,
-                                              int tid) {
-#pragma unroll
-  for (int j = 0; j < BN / 16; ++j) {
-    const int idx = tid + 128 * j;
-    const int r = idx >> 3, c = idx & 7;
-    const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
-    const float2 s = sc[(c >> 2) * BN + r];
-    *reinterpret_cast<uint4*>(bst + r * 128 + ((c ^ (r & 7)) << 4)) = q4_chunk(nib, s.x, s.y);
-  }
+// K-major destination chunk (row r, 16-byte column chunk c) of a [rows][64] 128B-swizzled tile.
+__device__ __forceinline__ uint4* kmajor_chunk(uint8_t* bst, int r, int c) {
+  return reinterpret_cast<uint4*>(bst + r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// Q4_K, MN-major output; raw [64][BN/2] bytes, sc [BN/32][64] float2.
-template <int BN>
-__device__ __forceinline__ void dequant_q4_tn(const uint8_t* raw, const float2* sc, uint8_t* bst,
-                                              int tid) {
-  constexpr int CPR = BN / 8;
+// MN-major destination chunk (k-row k, 8-element mn chunk cn) of [64 k][BN mn] atoms.
+__device__ __forceinline__ uint4* mnmajor_chunk(uint8_t* bst, int k, int cn) {
+  const int atom = cn >> 3, ch = cn & 7;
+  return reinterpret_cast<uint4*>(bst + atom * 8192 + (k >> 3) * 1024 + (k & 7) * 128 + ((ch ^ (k & 7)) << 4));
+}
+
+template <int BN, int BMODE, int NT>
+__device__ __forceinline__ void dequant_stage(const uint8_t* raw, const uint8_t* sc, uint8_t* bst, int tid) {
+  constexpr int PER = BN * 8 / NT;
+  static_assert(BN * 8 % NT == 0, "dequant split");
 #pragma unroll
-  for (int j = 0; j < BN / 16; ++j) {
-    const int idx = tid + 128 * j;
-    const int k = idx / CPR, cn = idx % CPR;
-    const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + k * (BN / 2) + cn * 4);
-    const float2 s = sc[(cn >> 2) * 64 + k];
-    const int atom = cn >> 3, ch = cn & 7;
-    *reinterpret_cast<uint4*>(bst + atom * 8192 + (k >> 3) * 1024 + (k & 7) * 128 +
-                              ((ch ^ (k & 7)) << 4)) = q4_chunk(nib, s.x, s.y);
+  for (int j = 0; j < PER; ++j) {
+    const int idx = tid + NT * j;
+    if (BMODE == 2) {          // Q8_0 NT: raw [BN][64] int8, sc [2][BN] f32
+      const int r = idx >> 3, c = idx & 7;
+      const uint2 q = *reinterpret_cast<const uint2*>(raw + r * 64 + c * 8);
+      *kmajor_chunk(bst, r, c) = q8_chunk(q, reinterpret_cast<const float*>(sc)[(c >> 2) * BN + r]);
+    } else if (BMODE == 3) {   // Q8_0 TN: raw [64][BN] int8, sc [BN/32][64] f32
+      const int k = idx / (BN / 8), cn = idx % (BN / 8);
+      const uint2 q = *reinterpret_cast<const uint2*>(raw + k * BN + cn * 8);
+      *mnmajor_chunk(bst, k, cn) = q8_chunk(q, reinterpret_cast<const float*>(sc)[(cn >> 2) * 64 + k]);
+    } else if (BMODE == 4) {   // Q4_K NT: raw [BN][32] bytes, sc [2][BN] float2
+      const int r = idx >> 3, c = idx & 7;
+      const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + r * 32 + c * 4);
+      const float2 s = reinterpret_cast<const float2*>(sc)[(c >> 2) * BN + r];
+      *kmajor_chunk(bst, r, c) = q4_chunk(nib, s.x, s.y);
+    } else if (BMODE == 5) {   // Q4_K TN: raw [64][BN/2] bytes, sc [BN/32][64] float2
+      const int k = idx / (BN / 8), cn = idx % (BN / 8);
+      const uint32_t nib = *reinterpret_cast<const uint32_t*>(raw + k * (BN / 2) + cn * 4);
+      const float2 s = reinterpret_cast<const float2*>(sc)[(cn >> 2) * 64 + k];
+      *mnmajor_chunk(bst, k, cn) = q4_chunk(nib, s.x, s.y);
+    }
   }
 }
 
 // ------------------------------------------------------------------ the kernel
+// Persistent: gridDim.x CTAs walk the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...
+// (tile t -> m-tile t % tiles_m, n-tile t / tiles_m, so co-resident CTAs share B columns).
+// The accumulator is double-buffered in TMEM: the epilogue drains tile i while the MMA warp
+// accumulates tile i + 1.
 template <int BN, int STAGES, int BMODE, bool A_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_bs, const __grid_constant__ CUtensorMap tm_ea,
                    const __grid_constant__ CUtensorMap tm_eb, const GemmArgs args) {
   using T = BModeTraits<BMODE>;
   using L = GemmSmem<BN, STAGES, BMODE>;
+  using R = GemmRoles<BMODE>;
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA M=128 needs N % 16 == 0, 16..256");
   static_assert(!T::mn || BN % 64 == 0, "MN-major B tiles are built from 64-wide atoms");
-  static_assert(!T::quant || BN >= 32, "dequant split assumes BN >= 32");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -191,12 +185,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
   uint64_t* empty = full + STAGES;
   uint64_t* bready = empty + STAGES;
-  uint64_t* accum = bready + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  uint64_t* tfull = bready + STAGES;     // [2] accumulator ready for the epilogue
+  uint64_t* tempty = tfull + 2;          // [2] accumulator drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
+  const int tiles_m = (args.M + kBM - 1) / kBM;
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int ntiles = tiles_m * tiles_n;
   const int nkb = (args.K + kBK - 1) / kBK;   // a ragged last block reads TMA zero fill
   const int total = nkb + (args.has_ext ? 1 : 0);
 
@@ -204,9 +201,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
-      mbar_init(&bready[s], 128);
+      mbar_init(&bready[s], R::DQ_THREADS > 0 ? R::DQ_THREADS : 1);
     }
-    mbar_init(accum, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 32 * R::EPI_WARPS);
+    }
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   __syncthreads();
   tc_fence_after();
-  const uint32_t taddr = *tmem_slot;
+  const uint32_t tbase = *tmem_slot;
 
   auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
     if (*abort_flag) return false;
@@ -243,46 +243,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      for (int it = 0; it < total; ++it) {
-        const int s = it % STAGES;
-        const uint32_t use = (uint32_t)(it / STAGES);
-        if (it >= STAGES && !wait(&empty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) break;
-        uint8_t* a_st = smem + L::OFF_A + s * L::A_BYTES;
-        uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
-        if (it < nkb) {
-          const int k0 = it * kBK;
-          const uint32_t bbytes = T::quant ? (uint32_t)(L::RAW_BYTES + L::SC_BYTES) : (uint32_t)L::B_BYTES;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)L::A_BYTES + bbytes);
-          if (A_MN) {
-            tma_load_2d(a_st, &tm_a, &full[s], m0, k0);
-            tma_load_2d(a_st + 8192, &tm_a, &full[s], m0 + 64, k0);
-          } else {
-            tma_load_2d(a_st, &tm_a, &full[s], k0, m0);
-          }
-          uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
-          uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
-          if (BMODE == 0) {
-            tma_load_2d(b_st, &tm_b, &full[s], k0, n0);
-          } else if (BMODE == 1) {
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
+        for (int kb = 0; kb < total; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t use = (uint32_t)(it / STAGES);
+          if (it >= STAGES && !wait(&empty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) { ok = false; break; }
+          uint8_t* a_st = smem + L::OFF_A + s * L::A_BYTES;
+          uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
+          if (kb < nkb) {
+            const int k0 = kb * kBK;
+            const uint32_t bbytes = T::quant ? (uint32_t)(L::RAW_BYTES + L::SC_BYTES) : (uint32_t)L::B_BYTES;
+            mbar_arrive_expect_tx(&full[s], (uint32_t)L::A_BYTES + bbytes);
+            if (A_MN) {
+              tma_load_2d(a_st, &tm_a, &full[s], m0, k0);
+              tma_load_2d(a_st + 8192, &tm_a, &full[s], m0 + 64, k0);
+            } else {
+              tma_load_2d(a_st, &tm_a, &full[s], k0, m0);
+            }
+            uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
+            uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
+            if (BMODE == 0) {
+              tma_load_2d(b_st, &tm_b, &full[s], k0, n0);
+            } else if (BMODE == 1) {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_st + j * 8192, &tm_b, &full[s], n0 + 64 * j, k0);
-          } else if (BMODE == 2) {
-            tma_load_2d(raw, &tm_b, &full[s], k0, n0);
-            tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
-          } else if (BMODE == 3) {
-            tma_load_2d(raw, &tm_b, &full[s], n0, k0);
-            tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
-          } else if (BMODE == 4) {
-            tma_load_2d(raw, &tm_b, &full[s], k0 / 2, n0);
-            tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
+              for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_st + j * 8192, &tm_b, &full[s], n0 + 64 * j, k0);
+            } else if (BMODE == 2) {
+              tma_load_2d(raw, &tm_b, &full[s], k0, n0);
+              tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
+            } else if (BMODE == 3) {
+              tma_load_2d(raw, &tm_b, &full[s], n0, k0);
+              tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
+            } else if (BMODE == 4) {
+              tma_load_2d(raw, &tm_b, &full[s], k0 / 2, n0);
+              tma_load_2d(sc, &tm_bs, &full[s], n0, k0 / 32);
+            } else {
+              tma_load_2d(raw, &tm_b, &full[s], n0 / 2, k0);
+              tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
+            }
           } else {
-            tma_load_2d(raw, &tm_b, &full[s], n0 / 2, k0);
-            tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(L::A_BYTES + L::B_BYTES));
+            tma_load_2d(a_st, &tm_ea, &full[s], 0, m0);
+            tma_load_2d(b_st, &tm_eb, &full[s], 0, n0);
           }
-        } else {
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(L::A_BYTES + L::B_BYTES));
-          tma_load_2d(a_st, &tm_ea, &full[s], 0, m0);
-          tma_load_2d(b_st, &tm_eb, &full[s], 0, n0);
         }
       }
     }
@@ -291,124 +296,144 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
       const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
+      int it = 0, ti = 0;
       bool ok = true;
-      for (int it = 0; it < total && ok; ++it) {
-        const int s = it % STAGES;
-        const uint32_t use = (uint32_t)(it / STAGES);
-        if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
-        if (T::quant && it < nkb && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++ti) {
+        const int a = ti & 1;
+        const uint32_t ause = (uint32_t)(ti >> 1);
+        if (ti >= 2 && !wait(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
-        const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
-        if (it < nkb) {
+        const uint32_t d_tmem = tbase + (uint32_t)(a * L::ACC_COLS);
+        for (int kb = 0; kb < total; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t use = (uint32_t)(it / STAGES);
+          if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
+          if (T::quant && kb < nkb && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
+          const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
+          if (kb < nkb) {
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = A_MN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
-                                     : make_sdesc(a_addr + kk * 32, 16, 1024);
-            const uint64_t bd = T::mn ? make_sdesc(b_addr + kk * 2048, 8192, 1024)
-                                      : make_sdesc(b_addr + kk * 32, 16, 1024);
-            umma_bf16(taddr, ad, bd, idesc, (it > 0 || kk > 0) ? 1u : 0u);
-          }
-        } else {
-          umma_bf16(taddr, make_sdesc(a_addr, 16, 1024), make_sdesc(b_addr, 16, 1024), idesc_ext,
-                    total > 1 ? 1u : 0u);
-        }
-        umma_commit(&empty[s]);
-      }
-      if (ok) umma_commit(accum);
-    }
-  } else {
-    // ------------------------------------------------------------ dequant, then epilogue
-    const int tid = threadIdx.x - 64;
-    if (T::quant) {
-      for (int it = 0; it < nkb; ++it) {
-        const int s = it % STAGES;
-        const uint32_t use = (uint32_t)(it / STAGES);
-        if (!wait(&full[s], use & 1u, kErrTimeoutFull)) break;
-        const uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
-        const uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
-        uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
-        if (BMODE == 2) dequant_q8_nt<BN>(raw, reinterpret_cast<const float*>(sc), b_st, tid);
-        if (BMODE == 3) dequant_q8_tn<BN>(raw, reinterpret_cast<const float*>(sc), b_st, tid);
-        if (BMODE == 4) dequant_q4_nt<BN>(raw, reinterpret_cast<const float2*>(sc), b_st, tid);
-        if (BMODE == 5) dequant_q4_tn<BN>(raw, reinterpret_cast<const float2*>(sc), b_st, tid);
-        fence_proxy_async_smem();
-        mbar_arrive(&bready[s]);
-      }
-    }
-    const bool have = wait(accum, 0, kErrTimeoutAccum);
-    tc_fence_after();
-    const int q = warp & 3;
-    const int row = m0 + 32 * q + lane;
-    const bool row_ok = have && row < args.M;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + ((uint32_t)(32 * q) << 16) + (uint32_t)c0, v);
-      tmem_ld_wait();
-      const int nb = n0 + c0;
-      if (!row_ok || nb >= args.N) continue;
-      float f[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = nb + j;
-        float x = __uint_as_float(v[j]) * args.alpha;
-        if (n < args.N) {
-          if (args.col_scale) x *= __ldg(args.col_scale + n);
-          if (args.col_bias) x += __ldg(args.col_bias + n);
-        }
-        f[j] = x;
-      }
-      const bool full16 = nb + 16 <= args.N;
-      if (args.out) {
-        if (!args.out_trans) {
-          float* dst = args.out + (long)row * args.ldo + nb;
-          if (full16 && (args.ldo % 4 == 0)) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-              if (args.accumulate) {
-                const float4 p = *reinterpret_cast<const float4*>(dst + j);
-                o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-              }
-              *reinterpret_cast<float4*>(dst + j) = o;
+            for (int kk = 0; kk < kBK / 16; ++kk) {
+              const uint64_t ad = A_MN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
+                                       : make_sdesc(a_addr + kk * 32, 16, 1024);
+              const uint64_t bd = T::mn ? make_sdesc(b_addr + kk * 2048, 8192, 1024)
+                                        : make_sdesc(b_addr + kk * 32, 16, 1024);
+              umma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
             }
           } else {
-            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = args.accumulate ? dst[j] + f[j] : f[j];
+            umma_bf16(d_tmem, make_sdesc(a_addr, 16, 1024), make_sdesc(b_addr, 16, 1024), idesc_ext,
+                      total > 1 ? 1u : 0u);
           }
-        } else {
-          for (int j = 0; j < 16 && nb + j < args.N; ++j) {
-            float* dst = args.out + (long)(nb + j) * args.ldo + row;
-            *dst = args.accumulate ? *dst + f[j] : f[j];
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[a]);
+      }
+    }
+  } else if (warp < 2 + R::EPI_WARPS) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;   // TMEM lane quarter this warp may access
+    int ti = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
+      const int a = ti & 1;
+      const uint32_t ause = (uint32_t)(ti >> 1);
+      const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
+      const bool have = wait(&tfull[a], ause & 1u, kErrTimeoutAccum);
+      tc_fence_after();
+      const int row = m0 + 32 * q + lane;
+      const bool row_ok = have && row < args.M;
+      const uint32_t tacc = tbase + (uint32_t)(a * L::ACC_COLS) + ((uint32_t)(32 * q) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tacc + (uint32_t)c0, v);
+        tmem_ld_wait();
+        const int nb = n0 + c0;
+        if (!row_ok || nb >= args.N) continue;
+        float f[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int n = nb + j;
+          float x = __uint_as_float(v[j]) * args.alpha;
+          if (n < args.N) {
+            if (args.col_scale) x *= __ldg(args.col_scale + n);
+            if (args.col_bias) x += __ldg(args.col_bias + n);
+          }
+          f[j] = x;
+        }
+        const bool full16 = nb + 16 <= args.N;
+        if (args.out) {
+          if (!args.out_trans) {
+            float* dst = args.out + (long)row * args.ldo + nb;
+            if (full16 && (args.ldo % 4 == 0)) {
+#pragma unroll
+              for (int j = 0; j < 16; j += 4) {
+                float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+                if (args.accumulate) {
+                  const float4 p = *reinterpret_cast<const float4*>(dst + j);
+                  o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+                }
+                *reinterpret_cast<float4*>(dst + j) = o;
+              }
+            } else {
+              for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = args.accumulate ? dst[j] + f[j] : f[j];
+            }
+          } else {
+            for (int j = 0; j < 16 && nb + j < args.N; ++j) {
+              float* dst = args.out + (long)(nb + j) * args.ldo + row;
+              *dst = args.accumulate ? *dst + f[j] : f[j];
+            }
+          }
+        }
+        if (args.out_bf) {
+          if (!args.out_bf_trans) {
+            __nv_bfloat16* dst = args.out_bf + (long)row * args.ldo_bf + nb;
+            if (full16 && (args.ldo_bf % 8 == 0)) {
+              uint4 o0, o1;
+              o0.x = pack_bf16x2(f[0], f[1]);   o0.y = pack_bf16x2(f[2], f[3]);
+              o0.z = pack_bf16x2(f[4], f[5]);   o0.w = pack_bf16x2(f[6], f[7]);
+              o1.x = pack_bf16x2(f[8], f[9]);   o1.y = pack_bf16x2(f[10], f[11]);
+              o1.z = pack_bf16x2(f[12], f[13]); o1.w = pack_bf16x2(f[14], f[15]);
+              *reinterpret_cast<uint4*>(dst) = o0;
+              *reinterpret_cast<uint4*>(dst + 8) = o1;
+            } else {
+              for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __float2bfloat16_rn(f[j]);
+            }
+          } else {
+            for (int j = 0; j < 16 && nb + j < args.N; ++j)
+              args.out_bf[(long)(nb + j) * args.ldo_bf + row] = __float2bfloat16_rn(f[j]);
           }
         }
       }
-      if (args.out_bf) {
-        if (!args.out_bf_trans) {
-          __nv_bfloat16* dst = args.out_bf + (long)row * args.ldo_bf + nb;
-          if (full16 && (args.ldo_bf % 8 == 0)) {
-            uint4 o0, o1;
-            o0.x = pack_bf16x2(f[0], f[1]);   o0.y = pack_bf16x2(f[2], f[3]);
-            o0.z = pack_bf16x2(f[4], f[5]);   o0.w = pack_bf16x2(f[6], f[7]);
-            o1.x = pack_bf16x2(f[8], f[9]);   o1.y = pack_bf16x2(f[10], f[11]);
-            o1.z = pack_bf16x2(f[12], f[13]); o1.w = pack_bf16x2(f[14], f[15]);
-            *reinterpret_cast<uint4*>(dst) = o0;
-            *reinterpret_cast<uint4*>(dst + 8) = o1;
-          } else {
-            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __float2bfloat16_rn(f[j]);
-          }
-        } else {
-          for (int j = 0; j < 16 && nb + j < args.N; ++j)
-            args.out_bf[(long)(nb + j) * args.ldo_bf + row] = __float2bfloat16_rn(f[j]);
+      tc_fence_before();
+      mbar_arrive(&tempty[a]);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant warps (quant modes)
+    if constexpr (T::quant) {
+      const int tid = threadIdx.x - 32 * (2 + R::EPI_WARPS);
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < total; ++kb, ++it) {
+          if (kb >= nkb) continue;   // the extension stage is loaded as bf16 by TMA
+          const int s = it % STAGES;
+          const uint32_t use = (uint32_t)(it / STAGES);
+          if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
+          const uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
+          const uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
+          uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
+          dequant_stage<BN, BMODE, R::DQ_THREADS>(raw, sc, b_st, tid);
+          fence_proxy_async_smem();
+          mbar_arrive(&bready[s]);
         }
       }
     }
-    tc_fence_before();
   }
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(taddr, L::TMEM_COLS);
+    tmem_dealloc(tbase, L::TMEM_COLS);
   }
 }
 

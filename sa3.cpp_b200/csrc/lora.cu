@@ -75,13 +75,33 @@ __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __
   }
 }
 
-// AAt[r1][r2] = sum_i A[r1][i] A[r2][i] (f32 accumulate), one block of 256 threads.
+// AAt[r1][r2] = sum_i A[r1][i] A[r2][i] (f32 accumulate).  Block r1 of 16; each of its 256
+// threads sums a strided slice of `in` for all 16 r2, then the block reduces.
 __global__ void aat_kernel(const float* __restrict__ A, int rank, int64_t in, float* __restrict__ aat) {
-  const int r1 = threadIdx.x / R, r2 = threadIdx.x % R;
-  float s = 0.f;
-  if (r1 < rank && r2 < rank)
-    for (int64_t i = 0; i < in; ++i) s = fmaf(A[r1 * in + i], A[r2 * in + i], s);
-  aat[threadIdx.x] = s;
+  const int r1 = blockIdx.x;
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+  if (r1 < rank) {
+    for (int64_t i = threadIdx.x; i < in; i += blockDim.x) {
+      const float a1 = A[(int64_t)r1 * in + i];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = r < rank ? fmaf(a1, A[(int64_t)r * in + i], acc[r]) : 0.f;
+    }
+  }
+  __shared__ float part[8][R];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float v = warp_sum(acc[r]);
+    if (lane == 0) part[wid][r] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < R) {
+    float v = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += part[w][threadIdx.x];
+    aat[r1 * R + threadIdx.x] = v;
+  }
 }
 
 // DoRA-rows norm per output row o (src/dit.h:126-144):
@@ -219,12 +239,14 @@ static unsigned grid1d(int64_t n, int threads, int cap = 148 * 16) {
 }
 
 int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err) {
+  ProfScope prof_(c, "cvt_bf16");
   cvt_bf16_kernel<<<grid1d(n / 4 + 1, 256), 256, 0, c->stream>>>(src, n, dst);
   return check_launch("cvt_bf16", err);
 }
 
 int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
                 __nv_bfloat16* trans, int ld_trans, std::string& err) {
+  ProfScope prof_(c, "pack_rank");
   dim3 blk(32, 8);
   pack_rank_kernel<<<(unsigned)((rows + 7) / 8), blk, 0, c->stream>>>(in, rows, mul, ext, mul_t, trans, ld_trans);
   return check_launch("pack_rank", err);
@@ -233,23 +255,27 @@ int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err) {
+  ProfScope prof_(c, "prep_adapter");
   prep_adapter_kernel<<<grid1d((in + out) * 64, 256), 256, 0, c->stream>>>(A, B, rank, in, out, a_bf, at_x, b_x, bt_bf);
   return check_launch("prep_adapter", err);
 }
 
 int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err) {
-  aat_kernel<<<1, 256, 0, c->stream>>>(A, rank, in, aat);
+  ProfScope prof_(c, "aat");
+  aat_kernel<<<R, 256, 0, c->stream>>>(A, rank, in, aat);
   return check_launch("aat", err);
 }
 
 int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                 const float* bns, const float* m, float s, float* nsq, float* g, std::string& err) {
+  ProfScope prof_(c, "dora_norm");
   dora_norm_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, bns, m, s, nsq, g);
   return check_launch("dora_norm", err);
 }
 
 int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
                    int64_t out, __nv_bfloat16* dz, float* dg, std::string& err) {
+  ProfScope prof_(c, "bwd_prologue");
   dim3 grid((unsigned)((out + 255) / 256), (unsigned)((S + kProTok - 1) / kProTok));
   bwd_prologue_kernel<<<grid, 256, 0, c->stream>>>(dy, y, bias, g, S, out, dz, dg);
   return check_launch("bwd_prologue", err);
@@ -258,12 +284,14 @@ int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, c
 int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
                float* dB, __nv_bfloat16* cb, float* c3, std::string& err) {
+  ProfScope prof_(c, "dora_bwd");
   dora_bwd_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, nsq, g, dg, s, dm,
                                                                        dm_acc, dB, cb, c3);
   return check_launch("dora_bwd", err);
 }
 
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err) {
+  ProfScope prof_(c, "dora_da_c3");
   dora_da_c3_kernel<<<(unsigned)(((int64_t)rank * in + 255) / 256), 256, 0, c->stream>>>(c3, A, rank, in, dA);
   return check_launch("dora_da_c3", err);
 }

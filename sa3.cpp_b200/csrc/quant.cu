@@ -125,7 +125,21 @@ __global__ void row_norms_kernel(const Weight w, float eps, float* __restrict__ 
   }
 }
 
+// bf16 operand copy of a quantized weight: the exact f32 dequantized value, rounded once.
+__global__ void dequant_bf16_kernel(const Weight w, __nv_bfloat16* __restrict__ dst) {
+  const int64_t n = w.in * w.out;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x)
+    dst[k] = __float2bfloat16_rn(wval(w, k / w.in, k % w.in));
+}
+
+int weight_cache_bf16(Ctx* c, Weight* w, std::string& err) {
+  ProfScope prof_(c, "weight cache");
+  dequant_bf16_kernel<<<1184, 256, 0, c->stream>>>(*w, w->bf16);
+  return check_launch("weight cache", err);
+}
+
 int weight_repack(Ctx* c, Weight* w, std::string& err) {
+  ProfScope prof_(c, "weight repack");
   const cudaStream_t st = c->stream;
   if (w->type == kTypeQ8_0) {
     const int64_t nblk = w->in / 32 * w->out;
@@ -147,11 +161,13 @@ int weight_repack(Ctx* c, Weight* w, std::string& err) {
 }
 
 int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err) {
+  ProfScope prof_(c, "dequant");
   dequant_kernel<<<1184, 256, 0, c->stream>>>(*w, dst);
   return check_launch("dequant", err);
 }
 
 int weight_row_norms(Ctx* c, const Weight* w, float eps, float* nsq, float* nrm, std::string& err) {
+  ProfScope prof_(c, "row norms");
   row_norms_kernel<<<(unsigned)((w->out + 7) / 8), 256, 0, c->stream>>>(*w, eps, nsq, nrm);
   return check_launch("row norms", err);
 }

@@ -24,14 +24,25 @@ struct Weight {
   void* raw = nullptr;               // F16/F32: the original values (dequant probe, row norms)
   int8_t* codes = nullptr;           // Q8_0 int8 [out][in] | Q4_K nibble pairs [out][in/2]
   float* scales = nullptr;           // Q8_0 f32 [in/32][out] | Q4_K float2 [in/32][out]
-  __nv_bfloat16* bf16 = nullptr;     // F16/F32: bf16 [out][in] operand copy
-  Ctx* owner = nullptr;
+  __nv_bfloat16* bf16 = nullptr;     // bf16 [out][in] operand copy (F16/F32 always; Q8_0/Q4_K
+                                     // when the context keeps a dequantized cache)
+  int device = 0;
 };
 
 // Growable device scratch owned by a context.
 struct Scratch {
   void* ptr = nullptr;
   size_t bytes = 0;
+};
+
+// Per launch-class counters (the counterpart of the reference's SA3_TRAIN_PROFILE timers,
+// src/train_loop.h:314-437): launches are always counted; with timing on, every launch is
+// bracketed by CUDA events on the context's stream.
+struct ProfEntry {
+  std::string name;
+  long long launches = 0;
+  double ms = 0.0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
 };
 
 struct Ctx {
@@ -41,6 +52,20 @@ struct Ctx {
   int* d_err = nullptr;              // device error word written by bounded waits
   std::vector<Scratch> scratch;      // indexed by the slot enums of the callers
   size_t sm_count = 148;
+  bool timing = false;
+  bool weight_cache = true;          // quantized weights keep a dequantized bf16 operand copy
+  bool smem_dequant = false;         // force the in-smem dequant GEMM path for quantized weights
+  std::vector<ProfEntry> prof;
+  std::vector<cudaEvent_t> ev_pool;
+};
+
+// RAII bracket around one kernel launch of class `name`.
+struct ProfScope {
+  Ctx* c;
+  int idx = -1;
+  cudaEvent_t e0 = nullptr;
+  ProfScope(Ctx* ctx, const char* name);
+  ~ProfScope();
 };
 
 // Run-time lookup of the driver entry point (the library does not link libcuda, so it loads on
@@ -64,6 +89,7 @@ inline int check_launch(const char* what, std::string& err) {
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
 
 int weight_repack(Ctx* c, Weight* w, std::string& err);
+int weight_cache_bf16(Ctx* c, Weight* w, std::string& err);
 int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err);
 int weight_row_norms(Ctx* c, const Weight* w, float eps, float* nsq, float* nrm, std::string& err);
 
@@ -102,6 +128,7 @@ struct GemmDesc {
   long ldo_bf = 0;
   int out_bf_trans = 0;
   int bn = 128;         // N tile (16, 128)
+  const char* name = "gemm";   // launch class for the profiler
 };
 
 int gemm(Ctx* c, const GemmDesc& d, std::string& err);

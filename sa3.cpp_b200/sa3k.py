@@ -19,8 +19,9 @@ ABI_SYMBOLS = (
     "sa3k_version", "sa3k_ctx_create", "sa3k_ctx_destroy", "sa3k_ctx_set_stream", "sa3k_sync",
     "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_linear_fwd",
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
-    "sa3k_average_clip_adamw",
+    "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
 )
+OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT = 1, 2
 
 
 class Sa3kError(RuntimeError):
@@ -30,6 +31,10 @@ class Sa3kError(RuntimeError):
 class Adapter(ctypes.Structure):
     _fields_ = [("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("magnitude", ctypes.c_void_p),
                 ("base_norm_sq", ctypes.c_void_p), ("scale", ctypes.c_float), ("rank", ctypes.c_int)]
+
+
+class ProfileEntry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
 
 
 class AdamWParams(ctypes.Structure):
@@ -65,6 +70,9 @@ def lib():
         L.sa3k_adamw.argtypes = [P, P, P, P, P, I64, ctypes.POINTER(AdamWParams), I, E, I]
         L.sa3k_average_clip_adamw.argtypes = [P, P, P, P, P, I64, I, ctypes.POINTER(AdamWParams), I,
                                               ctypes.POINTER(ctypes.c_double), E, I]
+        L.sa3k_profile_enable.argtypes = [P, I, E, I]
+        L.sa3k_ctx_set_option.argtypes = [P, I, I64, E, I]
+        L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
             if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free"):
                 getattr(L, name).restype = I
@@ -104,6 +112,10 @@ class Context:
         err = ctypes.create_string_buffer(256)
         _check(lib().sa3k_ctx_set_stream(self._h, ctypes.c_void_p(stream_handle), err, 256), err)
 
+    def set_option(self, option, value):
+        err = ctypes.create_string_buffer(256)
+        _check(lib().sa3k_ctx_set_option(self._h, option, int(value), err, 256), err)
+
     def sync(self):
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_sync(self._h, err, 512), err)
@@ -118,6 +130,19 @@ class Context:
             self.close()
         except Exception:
             pass
+
+    def profile_enable(self, timing=True):
+        err = ctypes.create_string_buffer(256)
+        _check(lib().sa3k_profile_enable(self._h, 1 if timing else 0, err, 256), err)
+
+    def profile_read(self):
+        """{class name: (launches, total_ms)} since the last profile_enable."""
+        err = ctypes.create_string_buffer(256)
+        n = ctypes.c_int(0)
+        _check(lib().sa3k_profile_read(self._h, None, 0, ctypes.byref(n), err, 256), err)
+        arr = (ProfileEntry * max(n.value, 1))()
+        _check(lib().sa3k_profile_read(self._h, arr, n.value, ctypes.byref(n), err, 256), err)
+        return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(n.value)}
 
     # -------------------------------------------------------------------- weights
     def upload(self, raw_bytes, qtype, inn, out):

@@ -79,6 +79,16 @@ def test_row_norms(ctx, qtype):
     np.testing.assert_allclose(nrm.cpu().numpy(), ref_nrm, rtol=1e-6)
 
 
+@pytest.fixture(params=["bf16_cache", "smem_dequant"])
+def operand_path(request, ctx):
+    """Run a test through both operand paths of the quantized GEMMs (identical numerics)."""
+    import sa3k
+    if request.param == "smem_dequant":
+        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 1)
+    yield request.param
+    ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
+
+
 def _run(ctx, qtype, mode, S, inn, out, rank, seed=3, api="fwd_bwd"):
     import torch
     c = _case(qtype, S, inn, out, rank, seed)
@@ -116,24 +126,24 @@ def _run(ctx, qtype, mode, S, inn, out, rank, seed=3, api="fwd_bwd"):
 
 @pytest.mark.parametrize("qtype", ["q8_0", "q4_k", "f16", "f32"])
 @pytest.mark.parametrize("mode", ["plain", "lora", "dora"])
-def test_linear_fwd_bwd_small(ctx, qtype, mode):
+def test_linear_fwd_bwd_small(ctx, operand_path, qtype, mode):
     res = _run(ctx, qtype, mode, S=200, inn=512, out=384, rank=16)
     assert all(v < TOL for v in res.values()), res
 
 
 @pytest.mark.parametrize("rank", [2, 16])
-def test_linear_separate_fwd_then_bwd(ctx, rank):
+def test_linear_separate_fwd_then_bwd(ctx, operand_path, rank):
     res = _run(ctx, "q8_0", "dora", S=130, inn=256, out=512, rank=rank, api="separate")
     assert all(v < TOL for v in res.values()), res
 
 
-def test_linear_config1_q8_0_lora(ctx):
+def test_linear_config1_q8_0_lora(ctx, operand_path):
     # 1536 x 1536 Q8_0, 1024 tokens, LoRA r 16 / alpha 16
     res = _run(ctx, "q8_0", "lora", S=1024, inn=1536, out=1536, rank=16, seed=11)
     assert all(v < TOL for v in res.values()), res
 
 
-def test_linear_config2_q4_k_dora(ctx):
+def test_linear_config2_q4_k_dora(ctx, operand_path):
     # 1536 -> 6144 Q4_K, 2048 tokens, DoRA r 16 / alpha 16
     res = _run(ctx, "q4_k", "dora", S=2048, inn=1536, out=6144, rank=16, seed=12)
     assert all(v < TOL for v in res.values()), res
@@ -184,3 +194,21 @@ def test_bad_arguments_raise(ctx):
     c = _case("q8_0", 8, 256, 128, 2, 7)
     with pytest.raises(sa3k.Sa3kError):
         ctx.upload(c["raw"], "q4_k", 256 + 64, 128)      # Q4_K needs in % 256 == 0
+
+
+def test_smem_and_cache_paths_agree_bitwise(ctx):
+    """Both operand paths round the same exact f32 dequantized value once to bf16 and run the same
+    MMA sequence, so their forward outputs match bit for bit."""
+    import torch
+    import sa3k
+    c = _case("q4_k", 300, 512, 768, 16, 21)
+    outs = []
+    for smem in (0, 1):
+        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, smem)
+        w = ctx.upload(c["raw"], "q4_k", 512, 768)
+        y = torch.empty(300, 768, device="cuda")
+        ctx.linear_fwd(w, _dev(c["x"]), y)
+        ctx.sync()
+        outs.append(y.cpu().numpy())
+    ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))

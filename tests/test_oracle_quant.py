@@ -59,3 +59,18 @@ def test_dora_magnitude_known_answer():
     nsq, nrm = oracle.row_norms(w)
     assert 5.47 < nrm[0] < 5.48
     assert np.isclose(nsq[0], 30.0 + 4 * 1e-12)
+
+
+def test_package_encoder_q8_0_matches_gguf_py_bytes():
+    import gguf_blocks
+    g = np.load(os.path.join(GOLD, "q8_0.npz"))
+    assert np.array_equal(gguf_blocks.q8_0(g["x"]), g["raw"])
+
+
+def test_package_encoder_q4_k_is_a_valid_accurate_encoding():
+    import gguf_blocks
+    rng = np.random.default_rng(9)
+    w = rng.normal(0, 0.02, (16, 1536)).astype(np.float32)
+    raw = gguf_blocks.q4_k(w)
+    y = oracle.dequantize(raw, "q4_k", *w.shape)
+    assert np.linalg.norm(y - w) / np.linalg.norm(w) < 0.12
