@@ -64,9 +64,12 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
 int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len);
 
 /* Per launch-class counters of this context: every kernel launch is counted by class
- * ("linear.fwd", "linear.dx", "lora.dA", "adamw", ...); with timing != 0 each launch is also
- * bracketed by CUDA events on the context's stream.  Enabling (or disabling) resets the
- * counters.  Counterpart of the SA3_TRAIN_PROFILE phase timers (src/train_loop.h:314-437). */
+ * ("linear.fwd", "linear.dx", "lora.dA", "adamw", ...).  timing 1: each launch is also
+ * bracketed by CUDA events on the context's stream and read sums the elapsed times.
+ * timing 2 (graph): the events are recorded as event nodes of a CUDA graph being captured on
+ * the context's stream; after each replay, read reports that replay's per-class times.
+ * Enabling resets the counters.  Counterpart of the SA3_TRAIN_PROFILE phase timers
+ * (src/train_loop.h:314-437). */
 typedef struct sa3k_profile_entry {
   char name[48];
   int64_t launches;

@@ -221,6 +221,15 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   return 0;
 }
 
+// Record a timing event; inside a stream capture it must become an event-record node of the
+// graph (cudaEventRecordExternal), otherwise it would only be a capture dependency.
+static void record_event(cudaEvent_t e, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(st, &cs);
+  if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, st, cudaEventRecordExternal);
+  else cudaEventRecord(e, st);
+}
+
 ProfScope::ProfScope(Ctx* ctx, const char* name) : c(ctx) {
   for (size_t i = 0; i < c->prof.size(); ++i)
     if (c->prof[i].name == name) { idx = (int)i; break; }
@@ -238,7 +247,7 @@ ProfScope::ProfScope(Ctx* ctx, const char* name) : c(ctx) {
     }
     e0 = c->ev_pool.back();
     c->ev_pool.pop_back();
-    cudaEventRecord(e0, c->stream);
+    record_event(e0, c->stream);
   }
 }
 
@@ -247,20 +256,26 @@ ProfScope::~ProfScope() {
   cudaEvent_t e1;
   if (c->ev_pool.empty()) cudaEventCreate(&e1);
   else { e1 = c->ev_pool.back(); c->ev_pool.pop_back(); }
-  cudaEventRecord(e1, c->stream);
+  record_event(e1, c->stream);
   c->prof[(size_t)idx].pending.emplace_back(e0, e1);
 }
 
+// Eager mode (timing 1): add the elapsed times of the recorded pairs and recycle the events.
+// Graph mode (timing 2): the pairs were captured into a graph and are re-recorded by each
+// replay; report the most recent replay's times and keep the pairs.
 static void prof_collect(Ctx* c) {
   cudaStreamSynchronize(c->stream);
   for (ProfEntry& p : c->prof) {
+    if (c->timing_graph) p.ms = 0.0;
     for (auto& ev : p.pending) {
       float ms = 0.f;
       if (cudaEventElapsedTime(&ms, ev.first, ev.second) == cudaSuccess) p.ms += ms;
-      c->ev_pool.push_back(ev.first);
-      c->ev_pool.push_back(ev.second);
+      if (!c->timing_graph) {
+        c->ev_pool.push_back(ev.first);
+        c->ev_pool.push_back(ev.second);
+      }
     }
-    p.pending.clear();
+    if (!c->timing_graph) p.pending.clear();
   }
   cudaGetLastError();
 }
@@ -358,10 +373,18 @@ int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len) {
 
 int sa3k_profile_enable(sa3k_ctx* ctx, int timing, char* err, int err_len) {
   if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  if (timing < 0 || timing > 2) return fill_err(err, err_len, "timing must be 0, 1 or 2");
   cudaSetDevice(ctx->c.device);
+  if (ctx->c.timing_graph) {   // release the graph-owned event pairs
+    for (ProfEntry& p : ctx->c.prof)
+      for (auto& ev : p.pending) { ctx->c.ev_pool.push_back(ev.first); ctx->c.ev_pool.push_back(ev.second); }
+    for (ProfEntry& p : ctx->c.prof) p.pending.clear();
+    ctx->c.timing_graph = false;
+  }
   prof_collect(&ctx->c);
   ctx->c.prof.clear();
   ctx->c.timing = timing != 0;
+  ctx->c.timing_graph = timing == 2;
   return 0;
 }
 

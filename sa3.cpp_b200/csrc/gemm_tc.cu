@@ -62,10 +62,41 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
     attr_set = true;
   }
   const long tiles = (long)((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
-  const unsigned grid = (unsigned)(tiles < (long)c->sm_count ? tiles : (long)c->sm_count);
-  ProfScope prof_(c, d.name);
-  kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, args);
-  return check_launch("gemm_tc", err);
+  GemmArgs a = args;
+  // split-K when the output has too few tiles to fill the GPU and K is long
+  const int nkb = (d.K + kBK - 1) / kBK;
+  a.splits = 1;
+  a.kb_per_split = nkb > 0 ? nkb : 1;
+  a.partial = nullptr;
+  if (tiles * 2 <= (long)c->sm_count && nkb >= 8) {
+    int splits = (int)((long)c->sm_count / tiles);
+    if (splits > nkb / 4) splits = nkb / 4;        // keep >= 4 k-blocks per split
+    if (splits > 1) {
+      const int kps = (nkb + splits - 1) / splits;
+      splits = (nkb + kps - 1) / kps;
+      float* part = static_cast<float*>(scratch_get(c, kSlotSplitK, (size_t)splits * d.M * d.N * sizeof(float), err));
+      if (!part) return 1;
+      a.splits = splits;
+      a.kb_per_split = kps;
+      a.partial = part;
+    }
+  }
+  const long items = tiles * a.splits;
+  const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
+  {
+    ProfScope prof_(c, d.name);
+    kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, a);
+    if (check_launch("gemm_tc", err)) return 1;
+  }
+  if (a.splits > 1) {
+    ProfScope prof_(c, "splitk_reduce");
+    const long mn = (long)d.M * d.N;
+    long blocks = (mn + 255) / 256;
+    if (blocks > 148 * 8) blocks = 148 * 8;
+    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, c->stream>>>(a);
+    return check_launch("splitk_reduce", err);
+  }
+  return 0;
 }
 
 // N tile for the main GEMMs: the cheaper of 128 / 256 by a wave-quantized cost model.
@@ -172,6 +203,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
   a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans;
   a.err = c->d_err;
+  a.splits = 1;
+  a.kb_per_split = 1;
+  a.partial = nullptr;
 
   if (bn == 16) {
     if (bmode != 0) { err = "gemm: N tile 16 supports bf16 K-major B only"; return 1; }

@@ -46,6 +46,9 @@ struct GemmArgs {
   __nv_bfloat16* out_bf;    // bf16 output (nullable), same scale/bias as out
   long ldo_bf;
   int out_bf_trans;
+  int splits;               // split-K: work item = (tile, split); 1 = no split
+  int kb_per_split;         // 64-wide k-blocks per split
+  float* partial;           // split-K: raw f32 partial sums [splits][M][N] (epilogue deferred)
   int* err;                 // device error word
 };
 
@@ -163,9 +166,33 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* raw, const uint8_t*
   }
 }
 
+// ------------------------------------------------------------------ split-K reduction
+// out = epilogue(alpha * sum_s partial[s]) with the same column scale / bias / accumulate /
+// transpose / bf16 options as the GEMM epilogue.  Deterministic (fixed summation order).
+__global__ void splitk_reduce_kernel(const GemmArgs args) {
+  const long mn = (long)args.M * args.N;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / args.N), n = (int)(i % args.N);
+    float x = 0.f;
+    for (int sp = 0; sp < args.splits; ++sp) x += args.partial[(long)sp * mn + i];
+    x *= args.alpha;
+    if (args.col_scale) x *= args.col_scale[n];
+    if (args.col_bias) x += args.col_bias[n];
+    if (args.out) {
+      float* dst = args.out_trans ? args.out + (long)n * args.ldo + m : args.out + (long)m * args.ldo + n;
+      *dst = args.accumulate ? *dst + x : x;
+    }
+    if (args.out_bf) {
+      __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)n * args.ldo_bf + m : args.out_bf + (long)m * args.ldo_bf + n;
+      *dst = __float2bfloat16_rn(x);
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the kernel
-// Persistent: gridDim.x CTAs walk the output tiles t = blockIdx.x, blockIdx.x + gridDim.x, ...
-// (tile t -> m-tile t % tiles_m, n-tile t / tiles_m, so co-resident CTAs share B columns).
+// Persistent: gridDim.x CTAs walk the work items blockIdx.x, blockIdx.x + gridDim.x, ...; an item
+// is an output tile t (m-tile t % tiles_m, n-tile t / tiles_m, so co-resident CTAs share B
+// columns) and, with split-K, one K-range of it.
 // The accumulator is double-buffered in TMEM: the epilogue drains tile i while the MMA warp
 // accumulates tile i + 1.
 template <int BN, int STAGES, int BMODE, bool A_MN>
@@ -194,8 +221,16 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
   const int tiles_m = (args.M + kBM - 1) / kBM;
   const int tiles_n = (args.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
-  const int nkb = (args.K + kBK - 1) / kBK;   // a ragged last block reads TMA zero fill
-  const int total = nkb + (args.has_ext ? 1 : 0);
+  const int nitems = ntiles * args.splits;
+  const int nkb_all = (args.K + kBK - 1) / kBK;   // a ragged last block reads TMA zero fill
+  // item -> (tile, split); split s covers k-blocks [s*kps, min(nkb_all, (s+1)*kps)) and the last
+  // split also runs the K = 16 extension
+  auto item_kb = [&](int item, int& kb0, int& nkb, int& total) {
+    const int split = item / ntiles;
+    kb0 = split * args.kb_per_split;
+    nkb = min(nkb_all - kb0, args.kb_per_split);
+    total = nkb + ((args.has_ext && split == args.splits - 1) ? 1 : 0);
+  };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -245,8 +280,11 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        const int t = item % ntiles;
         const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
+        int kb0, nkb, total;
+        item_kb(item, kb0, nkb, total);
         for (int kb = 0; kb < total; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
@@ -254,7 +292,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
           uint8_t* a_st = smem + L::OFF_A + s * L::A_BYTES;
           uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
           if (kb < nkb) {
-            const int k0 = kb * kBK;
+            const int k0 = (kb0 + kb) * kBK;
             const uint32_t bbytes = T::quant ? (uint32_t)(L::RAW_BYTES + L::SC_BYTES) : (uint32_t)L::B_BYTES;
             mbar_arrive_expect_tx(&full[s], (uint32_t)L::A_BYTES + bbytes);
             if (A_MN) {
@@ -298,7 +336,9 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
       int it = 0, ti = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++ti) {
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++ti) {
+        int kb0, nkb, total;
+        item_kb(item, kb0, nkb, total);
         const int a = ti & 1;
         const uint32_t ause = (uint32_t)(ti >> 1);
         if (ti >= 2 && !wait(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
@@ -308,7 +348,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
           if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
-          if (T::quant && kb < nkb && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
+          if (T::quant && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
           const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
@@ -334,7 +374,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;   // TMEM lane quarter this warp may access
     int ti = 0;
-    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++ti) {
+    for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++ti) {
+      const int t = item % ntiles;
       const int a = ti & 1;
       const uint32_t ause = (uint32_t)(ti >> 1);
       const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
@@ -350,6 +391,18 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         tmem_ld_wait();
         const int nb = n0 + c0;
         if (!row_ok || nb >= args.N) continue;
+        if (args.partial) {   // split-K: raw sums, the reduce kernel applies the epilogue
+          float* dst = args.partial + ((long)(item / ntiles) * args.M + row) * args.N + nb;
+          if (nb + 16 <= args.N && (args.N % 4 == 0)) {
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
+                                                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+          } else {
+            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __uint_as_float(v[j]);
+          }
+          continue;
+        }
         float f[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -414,17 +467,23 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       const int tid = threadIdx.x - 32 * (2 + R::EPI_WARPS);
       int it = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
+        int kb0, nkb, total;
+        item_kb(item, kb0, nkb, total);
         for (int kb = 0; kb < total; ++kb, ++it) {
-          if (kb >= nkb) continue;   // the extension stage is loaded as bf16 by TMA
+          // Every stage use is observed (and acknowledged on bready), the extension stage too
+          // (it is loaded as bf16 by TMA and needs no work): skipping a phase would make the
+          // next parity wait on this barrier alias with an older phase.
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
           if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
-          const uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
-          const uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
-          uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
-          dequant_stage<BN, BMODE, R::DQ_THREADS>(raw, sc, b_st, tid);
-          fence_proxy_async_smem();
+          if (kb < nkb) {
+            const uint8_t* raw = smem + L::OFF_RAW + s * L::RAW_STRIDE;
+            const uint8_t* sc = smem + L::OFF_SC + s * L::SC_STRIDE;
+            uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
+            dequant_stage<BN, BMODE, R::DQ_THREADS>(raw, sc, b_st, tid);
+            fence_proxy_async_smem();
+          }
           mbar_arrive(&bready[s]);
         }
       }

@@ -199,14 +199,16 @@ __global__ void dora_bwd_kernel(const float* __restrict__ pt, const float* __res
       cb[(int64_t)r * out + o] = __float2bfloat16_rn(dt2 * b[r]);
     }
   }
-  // c3 = B^T diag(dt3) B over this block's rows: warp sums, then one shared atomic per warp
+  // c3 = B^T diag(dt3) B over this block's rows: warp sums, then one shared atomic per warp.
+  // Fully unrolled over the padded rank (b is zero beyond `rank`) so b stays in registers.
   const int lane = threadIdx.x & 31;
-#pragma unroll 1
-  for (int r = 0; r < rank; ++r) {
-#pragma unroll 1
-    for (int k = r; k < rank; ++k) {
-      const float v = warp_sum(dt3 * b[r] * b[k]);
-      if (lane == 0) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float br = dt3 * b[r];
+#pragma unroll
+    for (int k = r; k < R; ++k) {
+      const float v = warp_sum(br * b[k]);
+      if (lane == 0 && r < rank && k < rank) {
         atomicAdd(&sc3[r * R + k], v);
         if (k != r) atomicAdd(&sc3[k * R + r], v);
       }

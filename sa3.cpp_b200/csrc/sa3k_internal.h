@@ -53,6 +53,7 @@ struct Ctx {
   std::vector<Scratch> scratch;      // indexed by the slot enums of the callers
   size_t sm_count = 148;
   bool timing = false;
+  bool timing_graph = false;         // timing events live in a captured CUDA graph
   bool weight_cache = true;          // quantized weights keep a dequantized bf16 operand copy
   bool smem_dequant = false;         // force the in-smem dequant GEMM path for quantized weights
   std::vector<ProfEntry> prof;
@@ -84,6 +85,9 @@ inline int check_launch(const char* what, std::string& err) {
   }
   return 0;
 }
+
+// Scratch slots owned by a context (see api.cu for the linear path's slots).
+enum : int { kSlotSplitK = 63 };
 
 // Scratch slot `slot` of at least `bytes` (grows; contents are not preserved on growth).
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);

@@ -212,3 +212,39 @@ def test_smem_and_cache_paths_agree_bitwise(ctx):
         outs.append(y.cpu().numpy())
     ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
     assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+
+
+def test_linear_step_replays_from_cuda_graph(ctx):
+    """The whole forward + backward is capturable: replaying the captured graph on fresh inputs
+    reproduces an eager call on the same inputs (y and dx bit for bit; dA, dB and dm go through
+    f32 atomic column sums of the DoRA backward, so only to rounding)."""
+    import torch
+    c = _case("q8_0", 512, 768, 1024, 16, 31)
+    w = ctx.upload(c["raw"], "q8_0", 768, 1024)
+    A, B, m, bns = _dev(c["A"]), _dev(c["B"]), _dev(c["m"]), _dev(c["bns"])
+    ad = ctx.adapter(A, B, 1.0, m, bns)
+    x, dy = _dev(c["x"]), _dev(c["dy"])
+    outs = {k: torch.empty(*s, device="cuda") for k, s in
+            (("y", (512, 1024)), ("dx", (512, 768)), ("dA", (16, 768)), ("dB", (1024, 16)), ("dm", (1024,)))}
+
+    def run():
+        ctx.linear_fwd_bwd(w, x, dy, outs["y"], outs["dx"], ad=ad, dA=outs["dA"], dB=outs["dB"], dm=outs["dm"])
+
+    run()                       # eager warm-up sizes the scratch buffers
+    ctx.sync()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        run()
+    ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+    x.copy_(_dev(c["x"][::-1].copy()))          # new inputs for the replay
+    g.replay()
+    torch.cuda.synchronize()
+    got = {k: v.cpu().numpy().copy() for k, v in outs.items()}
+    run()
+    ctx.sync()
+    for k, v in outs.items():
+        if k in ("y", "dx"):
+            assert np.array_equal(got[k].view(np.uint32), v.cpu().numpy().view(np.uint32)), k
+        else:
+            assert rel_l2(got[k], v.cpu().numpy()) < 1e-5, k
