@@ -56,6 +56,9 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  * Both paths round the same f32 dequantized value once to bf16, so results are identical. */
 #define SA3K_OPT_WEIGHT_BF16_CACHE 1
 #define SA3K_OPT_SMEM_DEQUANT 2
+/* SA3K_OPT_GEMM_TILE_N  0 (default): the N tile of the large GEMMs comes from a wave-count cost
+ *       model; 128 or 256 fixes it (a tuning knob; results do not depend on it). */
+#define SA3K_OPT_GEMM_TILE_N 3
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded

@@ -53,6 +53,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
                   const CUtensorMap& tbs, const CUtensorMap& tea, const CUtensorMap& teb,
                   const GemmArgs& args, std::string& err) {
   using L = GemmSmem<BN, STAGES, BMODE>;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   using R = GemmRoles<BMODE>;
   auto kern = gemm_tc_kernel<BN, STAGES, BMODE, A_MN>;
   static bool attr_set = false;
@@ -81,11 +82,25 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
       a.partial = part;
     }
   }
+  // epilogue through TMA stores when the output is a single row-major tensor
+  CUtensorMap tout = ta;
+  a.tma_out = 0;
+  if (a.splits == 1) {
+    std::string e2;
+    if (d.out && !d.out_bf && !d.out_trans && (d.ldo % 4) == 0 &&
+        (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
+        !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d.out, d.N, d.M, d.ldo * 4, 32, 32, SW, "out", e2))
+      a.tma_out = 1;
+    else if (d.out_bf && !d.out && !d.out_bf_trans && BN >= 64 && (d.ldo_bf % 8) == 0 &&
+             (reinterpret_cast<uintptr_t>(d.out_bf) & 15) == 0 &&
+             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
+      a.tma_out = 2;
+  }
   const long items = tiles * a.splits;
   const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
   {
     ProfScope prof_(c, d.name);
-    kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, a);
+    kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, tout, a);
     if (check_launch("gemm_tc", err)) return 1;
   }
   if (a.splits > 1) {
@@ -122,7 +137,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
                      !(d.w->bf16 && !c->smem_dequant);
   int bn = d.bn;
-  if (bn == 128) bn = pick_bn(c, d.M, d.N);
+  if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N);
   if (!(bn == 16 || bn == 128 || bn == 256)) {
     err = "gemm: unsupported N tile";
     return 1;
@@ -206,6 +221,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.splits = 1;
   a.kb_per_split = 1;
   a.partial = nullptr;
+  a.tma_out = 0;
 
   if (bn == 16) {
     if (bmode != 0) { err = "gemm: N tile 16 supports bf16 K-major B only"; return 1; }

@@ -49,6 +49,8 @@ struct GemmArgs {
   int splits;               // split-K: work item = (tile, split); 1 = no split
   int kb_per_split;         // 64-wide k-blocks per split
   float* partial;           // split-K: raw f32 partial sums [splits][M][N] (epilogue deferred)
+  int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: bf16 `out_bf` via TMA
+                            //    store; 0: direct stores (split-K partials, transposed or dual outputs)
   int* err;                 // device error word
 };
 
@@ -87,7 +89,13 @@ struct GemmSmem {
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_STRIDE;
-  static constexpr int OFF_BAR = align_up(OFF_SC + STAGES * SC_STRIDE, 64);
+  // epilogue: two 4 KB staging buffers per epilogue warp (32 rows x 128 B, 128B-swizzled), the
+  // source of the TMA stores (or of the coalescing transpose on the direct path)
+  static constexpr int OFF_STAGE = align_up(OFF_SC + STAGES * SC_STRIDE, 1024);
+  static constexpr int STAGE_BYTES = 4096;
+  // two staging buffers per warp when they fit next to the pipeline stages, else one
+  static constexpr int STAGE_BUFS = (OFF_STAGE + 4 * 2 * STAGE_BYTES + 1024 + 256 <= 232448) ? 2 : 1;
+  static constexpr int OFF_BAR = OFF_STAGE + 4 * STAGE_BUFS * STAGE_BYTES;
   static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
   static constexpr int DYN = TOTAL + 1024;   // slack for 1024-byte alignment of the base
@@ -199,7 +207,8 @@ template <int BN, int STAGES, int BMODE, bool A_MN>
 __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_bs, const __grid_constant__ CUtensorMap tm_ea,
-                   const __grid_constant__ CUtensorMap tm_eb, const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tm_eb, const __grid_constant__ CUtensorMap tm_out,
+                   const GemmArgs args) {
   using T = BModeTraits<BMODE>;
   using L = GemmSmem<BN, STAGES, BMODE>;
   using R = GemmRoles<BMODE>;
@@ -372,7 +381,16 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     }
   } else if (warp < 2 + R::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
+    // Each warp drains its 32 TMEM lanes (32 output rows).  TMA path (args.tma_out): 32 f32 (or
+    // 64 bf16) columns per step are written into a 128B-swizzled 32-row staging buffer and sent
+    // with one asynchronous TMA store (reduce-add when accumulating); two buffers alternate.
+    // Direct path: the same staging buffer transposes each 32 x 32 block so every global store
+    // is one coalesced row segment; transposed outputs are already coalesced across lanes.
     const int q = warp & 3;   // TMEM lane quarter this warp may access
+    uint8_t* stg = smem + L::OFF_STAGE + (warp - 2) * L::STAGE_BUFS * L::STAGE_BYTES;
+    const bool split_out = args.partial != nullptr;
+    const int cstep = args.tma_out == 2 ? 64 : 32;
+    int nstore = 0;
     int ti = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++ti) {
       const int t = item % ntiles;
@@ -381,86 +399,137 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
       const bool have = wait(&tfull[a], ause & 1u, kErrTimeoutAccum);
       tc_fence_after();
-      const int row = m0 + 32 * q + lane;
-      const bool row_ok = have && row < args.M;
+      const int rbase = m0 + 32 * q;               // first row of this warp
       const uint32_t tacc = tbase + (uint32_t)(a * L::ACC_COLS) + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tacc + (uint32_t)c0, v);
-        tmem_ld_wait();
+      for (int c0 = 0; c0 < BN; c0 += cstep) {
+        float f[64];
         const int nb = n0 + c0;
-        if (!row_ok || nb >= args.N) continue;
-        if (args.partial) {   // split-K: raw sums, the reduce kernel applies the epilogue
-          float* dst = args.partial + ((long)(item / ntiles) * args.M + row) * args.N + nb;
-          if (nb + 16 <= args.N && (args.N % 4 == 0)) {
 #pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]),
-                                                                __uint_as_float(v[j + 2]), __uint_as_float(v[j + 3]));
+        for (int h = 0; h < 2; ++h) {
+          if (h == 1 && cstep == 32) break;
+          const int cc = c0 + 32 * h;
+          uint32_t v[32];
+          if (BN - cc >= 32) {
+            tmem_ld32(tacc + (uint32_t)cc, v);
           } else {
-            for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __uint_as_float(v[j]);
+            tmem_ld16(tacc + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           }
+          // column scale / bias for these 32 columns (uniform across the warp: broadcast loads)
+          float cs[32], cb[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) { cs[j] = args.alpha; cb[j] = 0.f; }
+          if (!split_out && (args.col_scale || args.col_bias) && nb + 32 * h + 32 <= args.N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              if (args.col_scale) {
+                const float4 x4 = __ldg(reinterpret_cast<const float4*>(args.col_scale + nb + 32 * h + j));
+                cs[j] *= x4.x; cs[j + 1] *= x4.y; cs[j + 2] *= x4.z; cs[j + 3] *= x4.w;
+              }
+              if (args.col_bias) {
+                const float4 x4 = __ldg(reinterpret_cast<const float4*>(args.col_bias + nb + 32 * h + j));
+                cb[j] = x4.x; cb[j + 1] = x4.y; cb[j + 2] = x4.z; cb[j + 3] = x4.w;
+              }
+            }
+          } else if (!split_out && (args.col_scale || args.col_bias)) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int n = nb + 32 * h + j;
+              if (n < args.N) {
+                if (args.col_scale) cs[j] *= args.col_scale[n];
+                if (args.col_bias) cb[j] = args.col_bias[n];
+              }
+            }
+          }
+          if (split_out) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) { cs[j] = 1.f; cb[j] = 0.f; }
+          }
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[32 * h + j] = __uint_as_float(v[j]) * cs[j] + cb[j];
+        }
+        if (!have || nb >= args.N) continue;
+        if (args.tma_out) {
+          // ---- TMA store path: swizzled staging (16-byte chunk c of row r at c ^ (r & 7))
+          uint8_t* buf = stg + (L::STAGE_BUFS == 2 ? (nstore & 1) : 0) * L::STAGE_BYTES;
+          if (nstore >= L::STAGE_BUFS) {
+            // the store that last used this buffer must have read it
+            if (lane == 0) {
+              if (L::STAGE_BUFS == 2) bulk_wait_read<1>();
+              else bulk_wait_read<0>();
+            }
+            __syncwarp();
+          }
+          if (args.tma_out == 1) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<float4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                  make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint4 o;
+              o.x = pack_bf16x2(f[8 * c], f[8 * c + 1]);
+              o.y = pack_bf16x2(f[8 * c + 2], f[8 * c + 3]);
+              o.z = pack_bf16x2(f[8 * c + 4], f[8 * c + 5]);
+              o.w = pack_bf16x2(f[8 * c + 6], f[8 * c + 7]);
+              *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = o;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if (args.accumulate) tma_reduce_add_2d(&tm_out, buf, nb, rbase);
+            else tma_store_2d(&tm_out, buf, nb, rbase);
+            bulk_commit();
+          }
+          ++nstore;
           continue;
         }
-        float f[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = nb + j;
-          float x = __uint_as_float(v[j]) * args.alpha;
-          if (n < args.N) {
-            if (args.col_scale) x *= __ldg(args.col_scale + n);
-            if (args.col_bias) x += __ldg(args.col_bias + n);
-          }
-          f[j] = x;
-        }
-        const bool full16 = nb + 16 <= args.N;
-        if (args.out) {
-          if (!args.out_trans) {
-            float* dst = args.out + (long)row * args.ldo + nb;
-            if (full16 && (args.ldo % 4 == 0)) {
-#pragma unroll
-              for (int j = 0; j < 16; j += 4) {
-                float4 o = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-                if (args.accumulate) {
-                  const float4 p = *reinterpret_cast<const float4*>(dst + j);
-                  o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
-                }
-                *reinterpret_cast<float4*>(dst + j) = o;
-              }
-            } else {
-              for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = args.accumulate ? dst[j] + f[j] : f[j];
-            }
-          } else {
-            for (int j = 0; j < 16 && nb + j < args.N; ++j) {
-              float* dst = args.out + (long)(nb + j) * args.ldo + row;
+        // ---- direct path
+        const int ncols = min(min(32, BN - c0), args.N - nb);
+        const int myrow = rbase + lane;
+        if (args.out && args.out_trans) {          // lanes are consecutive rows: coalesced
+          if (myrow < args.M)
+            for (int j = 0; j < ncols; ++j) {
+              float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
               *dst = args.accumulate ? *dst + f[j] : f[j];
             }
-          }
         }
-        if (args.out_bf) {
-          if (!args.out_bf_trans) {
-            __nv_bfloat16* dst = args.out_bf + (long)row * args.ldo_bf + nb;
-            if (full16 && (args.ldo_bf % 8 == 0)) {
-              uint4 o0, o1;
-              o0.x = pack_bf16x2(f[0], f[1]);   o0.y = pack_bf16x2(f[2], f[3]);
-              o0.z = pack_bf16x2(f[4], f[5]);   o0.w = pack_bf16x2(f[6], f[7]);
-              o1.x = pack_bf16x2(f[8], f[9]);   o1.y = pack_bf16x2(f[10], f[11]);
-              o1.z = pack_bf16x2(f[12], f[13]); o1.w = pack_bf16x2(f[14], f[15]);
-              *reinterpret_cast<uint4*>(dst) = o0;
-              *reinterpret_cast<uint4*>(dst + 8) = o1;
-            } else {
-              for (int j = 0; j < 16 && nb + j < args.N; ++j) dst[j] = __float2bfloat16_rn(f[j]);
+        if (args.out_bf && args.out_bf_trans) {
+          if (myrow < args.M)
+            for (int j = 0; j < ncols; ++j)
+              args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j]);
+        }
+        if (split_out || (args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
+          float* st32 = reinterpret_cast<float*>(stg);     // 32 x 32 f32, XOR-swizzled columns
+#pragma unroll
+          for (int j = 0; j < 32; ++j) st32[lane * 32 + (j ^ lane)] = f[j];
+          __syncwarp();
+          float* pbase = split_out ? args.partial + (long)(item / ntiles) * args.M * args.N : nullptr;
+          for (int r = 0; r < 32; ++r) {
+            const int row = rbase + r;
+            if (row >= args.M || lane >= ncols) continue;
+            const float x = st32[r * 32 + (lane ^ r)];
+            if (split_out) {
+              pbase[(long)row * args.N + nb + lane] = x;
+              continue;
             }
-          } else {
-            for (int j = 0; j < 16 && nb + j < args.N; ++j)
-              args.out_bf[(long)(nb + j) * args.ldo_bf + row] = __float2bfloat16_rn(f[j]);
+            if (args.out && !args.out_trans) {
+              float* dst = args.out + (long)row * args.ldo + nb + lane;
+              *dst = args.accumulate ? *dst + x : x;
+            }
+            if (args.out_bf && !args.out_bf_trans) args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x);
           }
+          __syncwarp();
         }
       }
       tc_fence_before();
       mbar_arrive(&tempty[a]);
     }
+    if (lane == 0) bulk_wait_all();       // staging buffers must outlive the in-flight stores
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ dequant warps (quant modes)
     if constexpr (T::quant) {

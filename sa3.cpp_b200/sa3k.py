@@ -21,7 +21,7 @@ ABI_SYMBOLS = (
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
 )
-OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT = 1, 2
+OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N = 1, 2, 3
 
 
 class Sa3kError(RuntimeError):
