@@ -145,6 +145,54 @@ int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_ada
                              int64_t S, float* y_host, float* dx_host, float* dA_host,
                              float* dB_host, float* dm_host, char* err, int err_len);
 
+/* A strided 4-D tensor [B][H][S][head_dim]: element (b, h, s, d) is at
+ * data + b*batch_stride + h*head_stride + s*row_stride + d (strides in elements).  This covers
+ * head-major buffers and the token-major [B][S][H*head_dim] projection outputs alike. */
+typedef struct sa3k_tensor4 {
+  void* data;
+  int64_t batch_stride, head_stride, row_stride;
+} sa3k_tensor4;
+
+/* o = softmax(scale * q k^T [+ band mask]) v per (batch, head), head_dim 64; q, k, v, o bf16.
+ * window < 0: dense (the DiT's sdpa); window >= 0: keys with |i - j| <= window only (the banded
+ * attention of BASELINE config 3).  lse [B*H][Sq] (f32, log2 units) is kept for the backward.
+ * Replaces nn::sdpa (src/nn.h:135-144) and the band of attn_sliding (src/nn.h:79-100). */
+int sa3k_attention_fwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale,
+                       int window, const sa3k_tensor4* q, const sa3k_tensor4* k,
+                       const sa3k_tensor4* v, const sa3k_tensor4* o, float* lse, char* err,
+                       int err_len);
+
+/* Backward of sa3k_attention_fwd for upstream dO (bf16): dq, dk, dv (f32; dk and dv may be NULL
+ * for a frozen key/value source such as the cross-attention context).  Replaces the
+ * SOFT_MAX_BACK / OUT_PROD chain ggml derives for nn::sdpa. */
+int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale,
+                       int window, const sa3k_tensor4* q, const sa3k_tensor4* k,
+                       const sa3k_tensor4* v, const sa3k_tensor4* o, const sa3k_tensor4* dO,
+                       const float* lse, const sa3k_tensor4* dq, const sa3k_tensor4* dk,
+                       const sa3k_tensor4* dv, char* err, int err_len);
+
+/* One head slice of a fused projection output, for sa3k_head_prep_{fwd,bwd}. */
+typedef struct sa3k_head_slice {
+  int col;              /* first column of the slice in y (a multiple of 64)               */
+  const float* gamma;   /* [64] qk RMSNorm weight, or NULL (no norm)                        */
+  int rope;             /* apply partial NeoX RoPE after the norm                           */
+  float* rstd;          /* [T][H] saved 1/rms per (token, head) when gamma != NULL          */
+} sa3k_head_slice;
+
+/* out[T][ncols] (bf16) = per-head prepared slices of y[T][ncols] (f32): RMSNorm over each head's
+ * 64 values with gamma (eps), then NeoX RoPE of the first `rot` (32 or 64) dims at position
+ * (token index mod tokens_per_sample), base `rope_base`.  Replaces the qknorm + rope_neox of
+ * dit_block (src/dit.h:195, 209-217; src/nn.h:53-59). */
+int sa3k_head_prep_fwd(sa3k_ctx* ctx, const float* y, int T, int ncols, int H,
+                       const sa3k_head_slice* slices, int nslices, int tokens_per_sample, float eps,
+                       int rot, float rope_base, void* out_bf16, char* err, int err_len);
+
+/* Backward of one slice: g[T][H*64] (f32, row stride g_ld) is the gradient w.r.t. the prepared
+ * slice; writes the gradient w.r.t. y into that slice of dy[T][ncols] (f32). */
+int sa3k_head_prep_bwd(sa3k_ctx* ctx, const float* g, int64_t g_ld, const float* y, int T, int ncols,
+                       int H, const sa3k_head_slice* slice, int tokens_per_sample, int rot,
+                       float rope_base, float* dy, char* err, int err_len);
+
 /* AdamW hyper-parameters, as TrainAdamWParams (src/train_optimizer.h:28-35). */
 typedef struct sa3k_adamw_params {
   float learning_rate, beta1, beta2, eps, weight_decay, grad_clip;

@@ -1,6 +1,8 @@
 // api.cu -- the sa3k C ABI (include/sa3k.h): contexts, weights, dit_lin forward / backward and
 // the optimizer, orchestrated over the tcgen05 GEMM engine and the small kernels.
 #include "../../include/sa3k.h"
+#include "attention.h"
+#include "linear.h"
 #include "lora_kernels.h"
 #include "sa3k_internal.h"
 
@@ -47,22 +49,13 @@ void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err) {
   return s.ptr;
 }
 
-// Scratch slots of the linear path.
+// Scratch slots of the C-ABI linear entry points.
 enum Slot : int {
-  kS_XBF = 0, kS_ABF, kS_ATX, kS_BX, kS_BTBF, kS_U, kS_EXTU, kS_UT, kS_PT, kS_AAT, kS_NSQ, kS_G,
-  kS_DZ, kS_DG, kS_DU, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_Y, kS_HOST_IO, kS_OPT,
+  kS_XBF = 0, kS_PREP, kS_U, kS_EXTU, kS_UT, kS_DZ, kS_DG, kS_DU, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_HOST_IO, kS_OPT,
   kS_COUNT
 };
 
 static int64_t pad64(int64_t v) { return (v + 63) / 64 * 64; }
-
-struct LinBufs {
-  __nv_bfloat16 *x_bf = nullptr, *a_bf = nullptr, *at_x = nullptr, *b_x = nullptr, *bt_bf = nullptr;
-  __nv_bfloat16 *ext_u = nullptr, *ut = nullptr, *dz = nullptr, *ext_du = nullptr, *dut = nullptr, *cb = nullptr;
-  float *u = nullptr, *pt = nullptr, *aat = nullptr, *nsq = nullptr, *g = nullptr, *dg = nullptr, *du = nullptr,
-        *c3 = nullptr;
-  int64_t s_pad = 0;
-};
 
 template <class T>
 static bool get(Ctx* c, int slot, int64_t count, T*& p, std::string& err) {
@@ -70,36 +63,8 @@ static bool get(Ctx* c, int slot, int64_t count, T*& p, std::string& err) {
   return p != nullptr;
 }
 
-static int lin_bufs(Ctx* c, int64_t S, int64_t in, int64_t out, bool adapter, bool dora, bool bwd,
-                    LinBufs& b, std::string& err) {
-  b.s_pad = pad64(S);
-  if (!get(c, kS_XBF, S * in, b.x_bf, err)) return 1;
-  if (adapter) {
-    if (!get(c, kS_ABF, 16 * in, b.a_bf, err) || !get(c, kS_ATX, in * 64, b.at_x, err) ||
-        !get(c, kS_BX, out * 64, b.b_x, err) || !get(c, kS_BTBF, 16 * out, b.bt_bf, err) ||
-        !get(c, kS_U, S * 16, b.u, err) || !get(c, kS_EXTU, S * 64, b.ext_u, err) ||
-        !get(c, kS_UT, 16 * b.s_pad, b.ut, err))
-      return 1;
-  }
-  if (dora) {
-    if (!get(c, kS_PT, 16 * out, b.pt, err) || !get(c, kS_AAT, 256, b.aat, err) ||
-        !get(c, kS_NSQ, out, b.nsq, err) || !get(c, kS_G, out, b.g, err))
-      return 1;
-  }
-  if (bwd) {
-    if (!get(c, kS_DZ, S * out, b.dz, err)) return 1;
-    if (dora && (!get(c, kS_DG, out, b.dg, err) || !get(c, kS_CB, 16 * out, b.cb, err) ||
-                 !get(c, kS_C3, 256, b.c3, err)))
-      return 1;
-    if (adapter && (!get(c, kS_DU, S * 16, b.du, err) || !get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
-                    !get(c, kS_DUT, 16 * b.s_pad, b.dut, err)))
-      return 1;
-  }
-  return 0;
-}
-
-// The shared body of linear forward / backward.  y_out: forward output (nullable = no forward);
-// y_in: the forward output consumed by the DoRA backward when no forward runs here.
+// The C-ABI linear: f32 activations in, the adapter prepared per call.  y_out: forward output
+// (null = no forward); y_in: the forward output the DoRA backward needs when no forward runs.
 static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const float* bias, const float* x,
                       const float* dy, int64_t S, float* y_out, const float* y_in, float* dx, float* dA,
                       float* dB, float* dm, int accumulate, std::string& err) {
@@ -113,112 +78,56 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (adapter && (ad->rank < 1 || ad->rank > 16 || !ad->A || !ad->B)) { err = "adapter rank must be 1..16 with A and B"; return 1; }
   if (dora && !ad->base_norm_sq) { err = "dora adapter needs base_norm_sq"; return 1; }
   if (bwd && !fwd && dora && !y_in) { err = "dora backward needs the forward output y"; return 1; }
-  const int rank = adapter ? ad->rank : 0;
-  const float s = adapter ? ad->scale : 0.f;
-  LinBufs b;
-  if (lin_bufs(c, S, in, out, adapter, dora, bwd, b, err)) return 1;
+  const int64_t s_pad = pad64(S);
+  __nv_bfloat16* x_bf;
+  if (!get(c, kS_XBF, S * in, x_bf, err)) return 1;
+  if (k_cvt_bf16(c, x, S * in, x_bf, err)) return 1;
 
-  if (k_cvt_bf16(c, x, S * in, b.x_bf, err)) return 1;
+  AdapterPrep prep;
+  float *u = nullptr;
+  __nv_bfloat16 *ext_u = nullptr, *ut = nullptr;
   if (adapter) {
-    if (k_prep_adapter(c, ad->A, ad->B, rank, in, out, b.a_bf, b.at_x, b.b_x, b.bt_bf, err)) return 1;
-    // u = x A^T  [S][16]
-    GemmDesc g;
-    g.M = (int)S; g.N = 16; g.K = (int)in;
-    g.a = b.x_bf; g.lda = in;
-    g.bsrc = kB_BF16_KMAJOR; g.b = b.a_bf; g.ldb = in;
-    g.out = b.u; g.ldo = 16; g.bn = 16;
-    g.name = "lora.u";
-    if (gemm(c, g, err)) return 1;
-    if (k_pack_rank(c, b.u, (int)S, s, b.ext_u, 1.0f, bwd ? b.ut : nullptr, (int)b.s_pad, err)) return 1;
+    prep.rank = ad->rank; prep.in = in; prep.out = out; prep.s = ad->scale;
+    prep.A = ad->A; prep.B = ad->B; prep.m = dora ? ad->magnitude : nullptr; prep.bns = ad->base_norm_sq;
+    void* mem = scratch_get(c, kS_PREP, adapter_prep_bytes(in, out, dora), err);
+    if (!mem) return 1;
+    adapter_bind(prep, mem);
+    if (adapter_prepare(c, w, prep, err)) return 1;
+    if (!get(c, kS_U, S * 16, u, err) || !get(c, kS_EXTU, S * 64, ext_u, err) || !get(c, kS_UT, 16 * s_pad, ut, err))
+      return 1;
   }
-  if (dora) {
-    // P^T = A W^T  [16][out] ; then the row norm and g = m / sqrt(nsq)
-    GemmDesc g;
-    g.M = 16; g.N = (int)out; g.K = (int)in;
-    g.a = b.a_bf; g.lda = in;
-    g.bsrc = kB_WEIGHT_NT; g.w = w;
-    g.out = b.pt; g.ldo = out;
-    g.name = "dora.P";
-    if (gemm(c, g, err)) return 1;
-    if (k_aat(c, ad->A, rank, in, b.aat, err)) return 1;
-    if (k_dora_norm(c, b.pt, ad->B, rank, out, b.aat, ad->base_norm_sq, ad->magnitude, s, b.nsq, b.g, err)) return 1;
-  }
-  if (fwd) {
-    GemmDesc g;
-    g.M = (int)S; g.N = (int)out; g.K = (int)in;
-    g.a = b.x_bf; g.lda = in;
-    g.bsrc = kB_WEIGHT_NT; g.w = w;
-    if (adapter) { g.ext_a = b.ext_u; g.ext_b = b.b_x; }
-    g.col_scale = dora ? b.g : nullptr;
-    g.col_bias = bias;
-    g.out = y_out; g.ldo = out;
-    g.name = "linear.fwd";
-    if (gemm(c, g, err)) return 1;
+  if (fwd || (bwd && adapter)) {
+    // the backward needs u^T, which the forward produces; a backward-only call recomputes it
+    LinearFwd f;
+    f.w = w; f.ad = adapter ? &prep : nullptr; f.bias = bias; f.x_bf = x_bf; f.M = S;
+    f.y = y_out; f.u = u; f.ext_u = ext_u; f.ut = ut; f.ut_ld = s_pad;
+    if (!fwd) {
+      // u only: run the rank-16 GEMM and pack (the main GEMM is skipped without an output)
+      GemmDesc g;
+      g.M = (int)S; g.N = 16; g.K = (int)in;
+      g.a = x_bf; g.lda = in;
+      g.bsrc = kB_BF16_KMAJOR; g.b = prep.a_bf; g.ldb = in;
+      g.out = u; g.ldo = 16; g.bn = 16;
+      g.name = "lora.u";
+      if (gemm(c, g, err)) return 1;
+      if (k_pack_rank(c, u, (int)S, prep.s, ext_u, 1.0f, ut, (int)s_pad, err)) return 1;
+    } else if (linear_forward(c, f, err)) {
+      return 1;
+    }
   }
   if (!bwd) return 0;
-
-  const float* y_used = fwd ? y_out : y_in;
-  if (dora && cudaMemsetAsync(b.dg, 0, sizeof(float) * out, c->stream) != cudaSuccess) return check_launch("memset", err);
-  if (k_bwd_prologue(c, dy, dora ? y_used : nullptr, bias, dora ? b.g : nullptr, S, out, b.dz, dora ? b.dg : nullptr, err))
+  LinearBwd b;
+  b.w = w; b.ad = adapter ? &prep : nullptr; b.bias = bias; b.x_bf = x_bf; b.y = fwd ? y_out : y_in; b.dy = dy;
+  b.M = S; b.ut = ut; b.ut_ld = s_pad;
+  b.dx = dx; b.dx_accumulate = accumulate;
+  b.dA = dA; b.dB = dB; b.dm = dm; b.grad_accumulate = accumulate;
+  if (!get(c, kS_DZ, S * out, b.dz, err)) return 1;
+  if (dora && (!get(c, kS_DG, out, b.dg, err) || !get(c, kS_CB, 16 * out, b.cb, err) || !get(c, kS_C3, 256, b.c3, err)))
     return 1;
-  if (adapter) {
-    // du = s dz B  [S][16]
-    GemmDesc g;
-    g.M = (int)S; g.N = 16; g.K = (int)out;
-    g.a = b.dz; g.lda = out;
-    g.bsrc = kB_BF16_KMAJOR; g.b = b.bt_bf; g.ldb = out;
-    g.alpha = s;
-    g.out = b.du; g.ldo = 16; g.bn = 16;
-    g.name = "lora.du";
-    if (gemm(c, g, err)) return 1;
-    if (k_pack_rank(c, b.du, (int)S, 1.0f, b.ext_du, 1.0f, b.dut, (int)b.s_pad, err)) return 1;
-  }
-  if (dx) {
-    // dx = dz W + du A  (the LoRA term as a K = 16 extension of the same MMA chain)
-    GemmDesc g;
-    g.M = (int)S; g.N = (int)in; g.K = (int)out;
-    g.a = b.dz; g.lda = out;
-    g.bsrc = kB_WEIGHT_TN; g.w = w;
-    if (adapter) { g.ext_a = b.ext_du; g.ext_b = b.at_x; }
-    g.out = dx; g.ldo = in; g.accumulate = accumulate;
-    g.name = "linear.dx";
-    if (gemm(c, g, err)) return 1;
-  }
-  if (!adapter) return 0;
-  {
-    // dB = s dz^T u  [out][rank]
-    GemmDesc g;
-    g.M = (int)out; g.N = rank; g.K = (int)S;
-    g.a = b.dz; g.lda = out; g.a_mn = 1;
-    g.bsrc = kB_BF16_KMAJOR; g.b = b.ut; g.ldb = b.s_pad;
-    g.alpha = s;
-    g.out = dB; g.ldo = rank; g.accumulate = accumulate; g.bn = 16;
-    g.name = "lora.dB";
-    if (gemm(c, g, err)) return 1;
-  }
-  {
-    // dA = du^T x  [rank][in]
-    GemmDesc g;
-    g.M = rank; g.N = (int)in; g.K = (int)S;
-    g.a = b.dut; g.lda = b.s_pad;
-    g.bsrc = kB_BF16_MNMAJOR; g.b = b.x_bf; g.ldb = in;
-    g.out = dA; g.ldo = in; g.accumulate = accumulate;
-    g.name = "lora.dA";
-    if (gemm(c, g, err)) return 1;
-  }
-  if (dora) {
-    if (cudaMemsetAsync(b.c3, 0, sizeof(float) * 256, c->stream) != cudaSuccess) return check_launch("memset", err);
-    if (k_dora_bwd(c, b.pt, ad->B, rank, out, b.aat, b.nsq, b.g, b.dg, s, dm, accumulate, dB, b.cb, b.c3, err)) return 1;
-    GemmDesc g;
-    g.M = rank; g.N = (int)in; g.K = (int)out;
-    g.a = b.cb; g.lda = out;
-    g.bsrc = kB_WEIGHT_TN; g.w = w;
-    g.out = dA; g.ldo = in; g.accumulate = 1;
-    g.name = "dora.dA";
-    if (gemm(c, g, err)) return 1;
-    if (k_dora_da_c3(c, b.c3, ad->A, rank, in, dA, err)) return 1;
-  }
-  return 0;
+  if (adapter && (!get(c, kS_DU, S * 16, b.du, err) || !get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
+                  !get(c, kS_DUT, 16 * s_pad, b.dut, err)))
+    return 1;
+  return linear_backward(c, b, err);
 }
 
 // Record a timing event; inside a stream capture it must become an event-record node of the
@@ -579,6 +488,99 @@ int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_ada
   }
   if (!ok) return fill_err(err, err_len, "device->host copy failed");
   if (cudaStreamSynchronize(st) != cudaSuccess) return fill_err(err, err_len, "linear step failed");
+  return 0;
+}
+
+static void set4(const sa3k_tensor4* t, const __nv_bfloat16*& p, long& sb, long& sh, long& ld) {
+  p = static_cast<const __nv_bfloat16*>(t->data);
+  sb = (long)t->batch_stride;
+  sh = (long)t->head_stride;
+  ld = (long)t->row_stride;
+}
+
+static int attn_args(int B, int H, int Sq, int Sk, int head_dim, float scale, int window, const sa3k_tensor4* q,
+                     const sa3k_tensor4* k, const sa3k_tensor4* v, const sa3k_tensor4* o, AttnArgs& a,
+                     std::string& err) {
+  if (!q || !k || !v || !o || !q->data || !k->data || !v->data || !o->data) { err = "NULL tensor"; return 1; }
+  if (B <= 0 || H <= 0 || Sq <= 0 || Sk <= 0) { err = "attention dims must be positive"; return 1; }
+  a.B = B; a.H = H; a.Sq = Sq; a.Sk = Sk; a.head_dim = head_dim; a.scale = scale; a.window = window;
+  set4(q, a.q, a.q_sb, a.q_sh, a.q_ld);
+  set4(k, a.k, a.k_sb, a.k_sh, a.k_ld);
+  set4(v, a.v, a.v_sb, a.v_sh, a.v_ld);
+  a.o = static_cast<__nv_bfloat16*>(o->data);
+  a.o_sb = (long)o->batch_stride; a.o_sh = (long)o->head_stride; a.o_ld = (long)o->row_stride;
+  for (long st : {a.q_ld, a.k_ld, a.v_ld, a.o_ld})
+    if (st % 8) { err = "attention rows must be 16-byte aligned (row_stride % 8 == 0)"; return 1; }
+  return 0;
+}
+
+int sa3k_attention_fwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale, int window,
+                       const sa3k_tensor4* q, const sa3k_tensor4* k, const sa3k_tensor4* v, const sa3k_tensor4* o,
+                       float* lse, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  AttnArgs a;
+  if (attn_args(B, H, Sq, Sk, head_dim, scale, window, q, k, v, o, a, e)) return fill_err(err, err_len, e);
+  a.lse = lse;
+  if (attn_forward(&ctx->c, a, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale, int window,
+                       const sa3k_tensor4* q, const sa3k_tensor4* k, const sa3k_tensor4* v, const sa3k_tensor4* o,
+                       const sa3k_tensor4* dO, const float* lse, const sa3k_tensor4* dq, const sa3k_tensor4* dk,
+                       const sa3k_tensor4* dv, char* err, int err_len) {
+  if (!ctx || !dO || !dq || !lse) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  AttnArgs a;
+  if (attn_args(B, H, Sq, Sk, head_dim, scale, window, q, k, v, o, a, e)) return fill_err(err, err_len, e);
+  a.lse = const_cast<float*>(lse);
+  set4(dO, a.dO, a.dO_sb, a.dO_sh, a.dO_ld);
+  a.dq = static_cast<float*>(dq->data); a.dq_sb = (long)dq->batch_stride; a.dq_sh = (long)dq->head_stride;
+  a.dq_ld = (long)dq->row_stride;
+  const bool kv = dk && dv && dk->data && dv->data;
+  if (kv) {
+    a.dk = static_cast<float*>(dk->data); a.dk_sb = (long)dk->batch_stride; a.dk_sh = (long)dk->head_stride;
+    a.dk_ld = (long)dk->row_stride;
+    a.dv = static_cast<float*>(dv->data); a.dv_sb = (long)dv->batch_stride; a.dv_sh = (long)dv->head_stride;
+    a.dv_ld = (long)dv->row_stride;
+  }
+  float* dsum = static_cast<float*>(scratch_get(&ctx->c, kS_OPT + 1, sizeof(float) * (size_t)B * H * Sq, e));
+  if (!dsum) return fill_err(err, err_len, e);
+  a.Dsum = dsum;
+  if (attn_backward(&ctx->c, a, kv, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_head_prep_fwd(sa3k_ctx* ctx, const float* y, int T, int ncols, int H, const sa3k_head_slice* slices,
+                       int nslices, int tps, float eps, int rot, float rope_base, void* out, char* err, int err_len) {
+  if (!ctx || !y || !slices || !out) return fill_err(err, err_len, "NULL argument");
+  if (nslices < 1 || nslices > 5) return fill_err(err, err_len, "1..5 slices");
+  cudaSetDevice(ctx->c.device);
+  HeadSlice hs[5];
+  for (int i = 0; i < nslices; ++i) {
+    hs[i].col = slices[i].col; hs[i].gamma = slices[i].gamma; hs[i].rope = slices[i].rope; hs[i].rstd = slices[i].rstd;
+    if (hs[i].col % 64 || hs[i].col + H * 64 > ncols) return fill_err(err, err_len, "slice outside y");
+  }
+  std::string e;
+  if (k_head_prep_fwd(&ctx->c, y, T, ncols, H, hs, nslices, tps, eps, rot, rope_base,
+                      static_cast<__nv_bfloat16*>(out), e))
+    return fill_err(err, err_len, e);
+  return 0;
+}
+
+int sa3k_head_prep_bwd(sa3k_ctx* ctx, const float* g, int64_t g_ld, const float* y, int T, int ncols, int H,
+                       const sa3k_head_slice* slice, int tps, int rot, float rope_base, float* dy, char* err,
+                       int err_len) {
+  if (!ctx || !g || !y || !slice || !dy) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  HeadSlice hs;
+  hs.col = slice->col; hs.gamma = slice->gamma; hs.rope = slice->rope; hs.rstd = slice->rstd;
+  std::string e;
+  if (k_head_prep_bwd(&ctx->c, g, (long)g_ld, y, T, ncols, H, hs, tps, rot, rope_base, dy, e))
+    return fill_err(err, err_len, e);
   return 0;
 }
 

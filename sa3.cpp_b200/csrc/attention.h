@@ -1,0 +1,84 @@
+// attention.h -- attention and DiT elementwise kernels shared by the C ABI and the DiT step.
+#pragma once
+
+#include "sa3k_internal.h"
+
+namespace sa3k {
+
+// Strided bf16 / f32 tensors: element (b, h, s, d) at ptr + b*sb + h*sh + s*ld + d.
+struct AttnArgs {
+  int B = 0, H = 0, Sq = 0, Sk = 0, head_dim = 64;
+  float scale = 0.125f;
+  int window = -1;                       // -1 dense, else keep |q - k| <= window
+  const __nv_bfloat16* q = nullptr; long q_sb = 0, q_sh = 0, q_ld = 0;
+  const __nv_bfloat16* k = nullptr; long k_sb = 0, k_sh = 0, k_ld = 0;
+  const __nv_bfloat16* v = nullptr; long v_sb = 0, v_sh = 0, v_ld = 0;
+  __nv_bfloat16* o = nullptr; long o_sb = 0, o_sh = 0, o_ld = 0;           // written by forward
+  float* lse = nullptr;                  // [B*H][Sq], log2 units (row max + log2 of row sum)
+  // backward
+  const __nv_bfloat16* dO = nullptr; long dO_sb = 0, dO_sh = 0, dO_ld = 0;
+  float* Dsum = nullptr;                 // [B*H][Sq] scratch: rowsum(dO o O)
+  float* dq = nullptr; long dq_sb = 0, dq_sh = 0, dq_ld = 0;
+  float* dk = nullptr; long dk_sb = 0, dk_sh = 0, dk_ld = 0;
+  float* dv = nullptr; long dv_sb = 0, dv_sh = 0, dv_ld = 0;
+};
+
+int attn_forward(Ctx* c, const AttnArgs& a, std::string& err);
+// dq always; dk / dv when want_dkdv (cross-attention to a frozen context needs only dq)
+int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err);
+
+// ------------------------------------------------------------------ DiT elementwise (dit_ops.cu)
+// h = rms_norm(x) * gamma * (1 + sc[sample]) + sh[sample]  -> bf16, saves rstd per row
+int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, const float* sc, const float* sh,
+                      long mod_stride, int tokens_per_sample, float eps, __nv_bfloat16* h, float* rstd,
+                      std::string& err);
+// gx += d/dx of the above for upstream dh (gamma, sc, sh are frozen)
+int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
+                      const float* sc, long mod_stride, int tokens_per_sample, float* gx, std::string& err);
+
+// Per-head q/k preparation of a fused projection output y[T][ncols] (f32): for each slice (a
+// column offset that is a multiple of the head width 64): rms-norm with gamma (if gamma), then
+// partial NeoX RoPE of the first `rot` dims (if rope); written as bf16 into out[T][ncols].
+struct HeadSlice {
+  int col = 0;            // first column of the slice
+  const float* gamma = nullptr;   // null: copy only
+  int rope = 0;           // apply RoPE after the norm
+  float* rstd = nullptr;  // [T][H] saved for the backward (norm slices)
+};
+int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                    int tokens_per_sample, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err);
+// Backward of one slice: g[T][H*64] (f32, gradient w.r.t. the prepared slice) -> dy slice of
+// dy[T][ncols] (f32, overwritten), using the forward input y and the saved rstd.
+int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& s,
+                    int tokens_per_sample, int rot, float rope_base, float* dy, std::string& err);
+
+// x_out = x_in + y * gate[sample]  (gate already sigmoid(1 - g)); x_out may alias x_in
+int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate, long gate_stride, int T, int D,
+                    int tokens_per_sample, float* x_out, std::string& err);
+// dy = gx * gate[sample]
+int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gate_stride, int T, int D, int tokens_per_sample,
+               float* dy, std::string& err);
+// out = x + y (elementwise, n values); out may alias either input
+int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err);
+
+// SwiGLU: f[T][2I] -> a[T][I] = f[:, :I] * silu(f[:, I:]) (bf16); backward da -> df (f32)
+int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err);
+int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err);
+
+// silu in place (f32) and its f32 -> bf16 copy for a following GEMM
+int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err);
+
+// mod[b][i] = ssg[i] + gcond[b][i] for i < 6*D, and the two gates sigmoid(1 - g) in place of
+// slots 2 and 5 (the adaLN-zero vectors of src/dit.h:174-193)
+int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err);
+
+// loss[b] = sum((vel - target)^2) / (io*T) per sample; dvel = 2 (vel - target) / (io*T)
+int k_mse(Ctx* c, const float* vel, const float* target, int B, long per_sample, float* loss, float* dvel,
+          std::string& err);
+
+// copy rows: dst[b*dst_rows_per + dst_off + r][:] = src[b*src_rows_per + src_off + r][:] for r < rows
+// (f32 or bf16 destination), used for the memory-token concat / drop of dit_head / dit_tail
+int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __nv_bfloat16* dst_bf,
+                int dst_rows_per, int dst_off, int B, int rows, int D, std::string& err);
+
+}  // namespace sa3k

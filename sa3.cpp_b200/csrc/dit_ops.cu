@@ -1,0 +1,388 @@
+// dit_ops.cu -- the memory-bound pieces of one DiT block, forward and backward.
+//
+// Each kernel restates a group of ggml ops of dit_block (src/dit.h:164-266) in the autodiff-safe
+// form the training graph uses, plus the derivative ggml_build_backward_expand produces for it:
+//   rms_norm + adaLN modulate   src/nn.h:40-42, src/dit.h:177-185    (RMS_NORM(_BACK), MUL, ADD)
+//   qk rms_norm + partial RoPE  src/dit.h:195, src/nn.h:53-59       (ROPE NEOX and its backward)
+//   gate + residual             src/dit.h:186-193, 223, 265          (h / (exp(g - 1) + 1))
+//   SwiGLU                      src/dit.h:259-264                    (SILU(_BACK), MUL)
+//   adaLN vectors               src/dit.h:174-176                    (ssg + gcond)
+//   MSE loss                    src/train_ckpt.h:226-228
+// All are vectorized row kernels (one warp per row or 128-bit grid-stride loops).
+#include "attention.h"
+#include "sa3k_common.cuh"
+
+namespace sa3k {
+namespace {
+
+__global__ void rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D, const float* __restrict__ gamma,
+                                       const float* __restrict__ sc, const float* __restrict__ sh, long mod_stride,
+                                       int tps, float eps, __nv_bfloat16* __restrict__ h, float* __restrict__ rstd) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int lane = threadIdx.x & 31;
+  const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
+  float ss = 0.f;
+  for (int i = lane; i < D / 4; i += 32) {
+    const float4 v = xr[i];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)D + eps);
+  if (lane == 0 && rstd) rstd[row] = r;
+  const int s = row / tps;
+  const float* scs = sc ? sc + (long)s * mod_stride : nullptr;
+  const float* shs = sh ? sh + (long)s * mod_stride : nullptr;
+  uint2* hr = reinterpret_cast<uint2*>(h + (long)row * D);
+  for (int i = lane; i < D / 4; i += 32) {
+    const float4 v = xr[i];
+    const float4 gm = reinterpret_cast<const float4*>(gamma)[i];
+    float o[4] = {v.x * r * gm.x, v.y * r * gm.y, v.z * r * gm.z, v.w * r * gm.w};
+    if (scs) {
+      const float4 a = reinterpret_cast<const float4*>(scs)[i];
+      const float4 b = reinterpret_cast<const float4*>(shs)[i];
+      o[0] = o[0] * (1.f + a.x) + b.x;
+      o[1] = o[1] * (1.f + a.y) + b.y;
+      o[2] = o[2] * (1.f + a.z) + b.z;
+      o[3] = o[3] * (1.f + a.w) + b.w;
+    }
+    uint2 pk;
+    pk.x = pack_bf16x2(o[0], o[1]);
+    pk.y = pack_bf16x2(o[2], o[3]);
+    hr[i] = pk;
+  }
+}
+
+__global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float* __restrict__ x,
+                                       const float* __restrict__ rstd, int T, int D, const float* __restrict__ gamma,
+                                       const float* __restrict__ sc, long mod_stride, int tps, float* __restrict__ gx) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= T) return;
+  const int lane = threadIdx.x & 31;
+  const float r = rstd[row];
+  const int s = row / tps;
+  const float* scs = sc ? sc + (long)s * mod_stride : nullptr;
+  const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
+  const float4* dr = reinterpret_cast<const float4*>(dh + (long)row * D);
+  float dot = 0.f;
+  for (int i = lane; i < D / 4; i += 32) {
+    const float4 v = xr[i], d = dr[i], gm = reinterpret_cast<const float4*>(gamma)[i];
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (scs) a = reinterpret_cast<const float4*>(scs)[i];
+    dot += d.x * gm.x * (1.f + a.x) * v.x + d.y * gm.y * (1.f + a.y) * v.y + d.z * gm.z * (1.f + a.z) * v.z +
+           d.w * gm.w * (1.f + a.w) * v.w;
+  }
+  dot = warp_sum(dot) * r / (float)D;   // mean(dn * n)
+  float4* gr = reinterpret_cast<float4*>(gx + (long)row * D);
+  for (int i = lane; i < D / 4; i += 32) {
+    const float4 v = xr[i], d = dr[i], gm = reinterpret_cast<const float4*>(gamma)[i];
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (scs) a = reinterpret_cast<const float4*>(scs)[i];
+    float4 gv = gr[i];
+    gv.x += r * (d.x * gm.x * (1.f + a.x) - v.x * r * dot);
+    gv.y += r * (d.y * gm.y * (1.f + a.y) - v.y * r * dot);
+    gv.z += r * (d.z * gm.z * (1.f + a.z) - v.z * r * dot);
+    gv.w += r * (d.w * gm.w * (1.f + a.w) - v.w * r * dot);
+    gr[i] = gv;
+  }
+}
+
+// RoPE angle of pair i (< rot/2) at position pos: pos * base^(-2i/rot)
+__device__ __forceinline__ void rope_cs(int pos, int i, int rot, float log2_base, float& c, float& s) {
+  const float freq = exp2f(-2.0f * (float)i / (float)rot * log2_base);
+  sincosf((float)pos * freq, &s, &c);
+}
+
+// One warp per (token, head, slice); lane l holds head elements l and l + 32.
+struct HeadSlices {
+  HeadSlice s[5];
+  int n;
+};
+
+__global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
+                                     int tps, float eps, int rot, float log2_base, __nv_bfloat16* __restrict__ out) {
+  const int nslices = slices.n;
+  const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const long total = (long)T * H * nslices;
+  if (wid >= total) return;
+  const int lane = threadIdx.x & 31;
+  const int si = (int)(wid % nslices);
+  const int h = (int)((wid / nslices) % H);
+  const int t = (int)(wid / ((long)nslices * H));
+  const HeadSlice sl = slices.s[si];
+  const long base = (long)t * ncols + sl.col + h * 64;
+  float a = y[base + lane], b = y[base + lane + 32];
+  if (sl.gamma) {
+    const float r = rsqrtf(warp_sum(a * a + b * b) / 64.f + eps);
+    if (lane == 0 && sl.rstd) sl.rstd[(long)t * H + h] = r;
+    a *= r * sl.gamma[lane];
+    b *= r * sl.gamma[lane + 32];
+  }
+  if (sl.rope) {
+    const int pos = t % tps;
+    if (rot == 32) {   // pairs (i, i + 16) for i < 16 live in lanes i and i ^ 16
+      const float pa = __shfl_xor_sync(0xffffffffu, a, 16);
+      float c, s;
+      rope_cs(pos, lane & 15, rot, log2_base, c, s);
+      a = lane < 16 ? a * c - pa * s : pa * s + a * c;
+    } else if (rot == 64) {   // pairs (i, i + 32) live in one lane
+      float c, s;
+      rope_cs(pos, lane, rot, log2_base, c, s);
+      const float na = a * c - b * s, nb = a * s + b * c;
+      a = na;
+      b = nb;
+    }
+  }
+  out[base + lane] = __float2bfloat16_rn(a);
+  out[base + lane + 32] = __float2bfloat16_rn(b);
+}
+
+__global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, const float* __restrict__ y, int T,
+                                     int ncols, int H, HeadSlice sl, int tps, int rot, float log2_base,
+                                     float* __restrict__ dy) {
+  const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (wid >= (long)T * H) return;
+  const int lane = threadIdx.x & 31;
+  const int h = (int)(wid % H), t = (int)(wid / H);
+  float ga = g[(long)t * g_ld + h * 64 + lane], gb = g[(long)t * g_ld + h * 64 + lane + 32];
+  const long base = (long)t * ncols + sl.col + h * 64;
+  if (sl.rope) {   // inverse rotation of the gradient
+    const int pos = t % tps;
+    if (rot == 32) {
+      const float pa = __shfl_xor_sync(0xffffffffu, ga, 16);
+      float c, s;
+      rope_cs(pos, lane & 15, rot, log2_base, c, s);
+      ga = lane < 16 ? ga * c + pa * s : -pa * s + ga * c;
+    } else if (rot == 64) {
+      float c, s;
+      rope_cs(pos, lane, rot, log2_base, c, s);
+      const float na = ga * c + gb * s, nb = -ga * s + gb * c;
+      ga = na;
+      gb = nb;
+    }
+  }
+  if (sl.gamma) {
+    const float r = sl.rstd[(long)t * H + h];
+    const float na = y[base + lane] * r, nb = y[base + lane + 32] * r;
+    const float da = ga * sl.gamma[lane], db = gb * sl.gamma[lane + 32];
+    const float mean = warp_sum(da * na + db * nb) / 64.f;
+    ga = r * (da - na * mean);
+    gb = r * (db - nb * mean);
+  }
+  dy[base + lane] = ga;
+  dy[base + lane + 32] = gb;
+}
+
+__global__ void gate_residual_kernel(const float* __restrict__ x_in, const float* __restrict__ y,
+                                     const float* __restrict__ gate, long gstride, int T, int D, int tps,
+                                     float* __restrict__ x_out) {
+  const long n4 = (long)T * D / 4;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const long e = i * 4;
+    const int t = (int)(e / D), cidx = (int)(e % D);
+    const float4 gv = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + cidx);
+    const float4 a = reinterpret_cast<const float4*>(x_in)[i];
+    const float4 b = reinterpret_cast<const float4*>(y)[i];
+    reinterpret_cast<float4*>(x_out)[i] = make_float4(a.x + b.x * gv.x, a.y + b.y * gv.y, a.z + b.z * gv.z, a.w + b.w * gv.w);
+  }
+}
+
+__global__ void gate_bwd_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride, int T,
+                                int D, int tps, float* __restrict__ dy) {
+  const long n4 = (long)T * D / 4;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const long e = i * 4;
+    const int t = (int)(e / D), cidx = (int)(e % D);
+    const float4 gv = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + cidx);
+    const float4 a = reinterpret_cast<const float4*>(gx)[i];
+    reinterpret_cast<float4*>(dy)[i] = make_float4(a.x * gv.x, a.y * gv.y, a.z * gv.z, a.w * gv.w);
+  }
+}
+
+__global__ void add_kernel(const float* __restrict__ x, const float* __restrict__ y, long n, float* __restrict__ out) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) out[i] = x[i] + y[i];
+}
+
+__device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+
+__global__ void swiglu_fwd_kernel(const float* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
+  const long n = (long)T * I;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / I, j = i % I;
+    const float v = f[t * 2 * I + j], gl = f[t * 2 * I + I + j];
+    a[i] = __float2bfloat16_rn(v * gl * sigm(gl));
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
+                                  float* __restrict__ df) {
+  const long n = (long)T * I;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / I, j = i % I;
+    const float v = f[t * 2 * I + j], gl = f[t * 2 * I + I + j];
+    const float sg = sigm(gl), d = da[i];
+    df[t * 2 * I + j] = d * gl * sg;
+    df[t * 2 * I + I + j] = d * v * sg * (1.f + gl * (1.f - sg));
+  }
+}
+
+__global__ void silu_bf16_kernel(const float* __restrict__ x, long n, __nv_bfloat16* __restrict__ out) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    out[i] = __float2bfloat16_rn(v * sigm(v));
+  }
+}
+
+__global__ void modulation_kernel(const float* __restrict__ ssg, const float* __restrict__ gcond, int B, int D,
+                                  float* __restrict__ mod) {
+  const long n = (long)B * 6 * D;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long j = i % (6L * D);
+    float v = ssg[j] + gcond[i];
+    const int slot = (int)(j / D);
+    if (slot == 2 || slot == 5) v = 1.f / (__expf(v - 1.f) + 1.f);   // h * sigmoid(1 - g)
+    mod[i] = v;
+  }
+}
+
+__global__ void mse_kernel(const float* __restrict__ vel, const float* __restrict__ tgt, long per, float inv,
+                           float* __restrict__ loss, float* __restrict__ dvel) {
+  const int b = blockIdx.y;
+  float acc = 0.f;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (long)gridDim.x * blockDim.x) {
+    const long e = (long)b * per + i;
+    const float d = vel[e] - tgt[e];
+    acc += d * d;
+    if (dvel) dvel[e] = 2.f * d * inv;
+  }
+  acc = warp_sum(acc);
+  __shared__ float part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) atomicAdd(loss + b, v * inv);
+  }
+}
+
+__global__ void copy_rows_kernel(const float* __restrict__ src, int src_rows_per, int src_off, float* __restrict__ dst,
+                                 __nv_bfloat16* __restrict__ dst_bf, int dst_rows_per, int dst_off, int B, int rows,
+                                 int D) {
+  const long n = (long)B * rows * D;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long d = i % D, r = (i / D) % rows, b = i / ((long)D * rows);
+    const float v = src[((long)b * src_rows_per + src_off + r) * D + d];
+    const long o = ((long)b * dst_rows_per + dst_off + r) * D + d;
+    if (dst) dst[o] = v;
+    if (dst_bf) dst_bf[o] = __float2bfloat16_rn(v);
+  }
+}
+
+unsigned gs(long n, int threads = 256) {
+  long b = (n + threads - 1) / threads;
+  if (b > 148 * 16) b = 148 * 16;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+
+}  // namespace
+
+int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, const float* sc, const float* sh,
+                      long mod_stride, int tps, float eps, __nv_bfloat16* h, float* rstd, std::string& err) {
+  if (D % 4) { err = "rms_norm: D % 4"; return 1; }
+  ProfScope prof_(c, "rmsnorm_mod_fwd");
+  rmsnorm_mod_fwd_kernel<<<(unsigned)((T + 7) / 8), 256, 0, c->stream>>>(x, T, D, gamma, sc, sh, mod_stride, tps, eps, h, rstd);
+  return check_launch("rmsnorm_mod_fwd", err);
+}
+
+int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
+                      const float* sc, long mod_stride, int tps, float* gx, std::string& err) {
+  ProfScope prof_(c, "rmsnorm_mod_bwd");
+  rmsnorm_mod_bwd_kernel<<<(unsigned)((T + 7) / 8), 256, 0, c->stream>>>(dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx);
+  return check_launch("rmsnorm_mod_bwd", err);
+}
+
+int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
+                    float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+  if (rot != 0 && rot != 32 && rot != 64) { err = "rope: rot must be 32 or 64"; return 1; }
+  if (nslices < 1 || nslices > 5) { err = "head_prep: 1..5 slices"; return 1; }
+  HeadSlices hs{};
+  for (int i = 0; i < nslices; ++i) hs.s[i] = slices[i];
+  hs.n = nslices;
+  ProfScope prof_(c, "head_prep_fwd");
+  const long warps = (long)T * H * nslices;
+  head_prep_fwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot,
+                                                                           log2f(rope_base), out);
+  return check_launch("head_prep_fwd", err);
+}
+
+int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
+                    int tps, int rot, float rope_base, float* dy, std::string& err) {
+  ProfScope prof_(c, "head_prep_bwd");
+  const long warps = (long)T * H;
+  head_prep_bwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot,
+                                                                           log2f(rope_base), dy);
+  return check_launch("head_prep_bwd", err);
+}
+
+int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate, long gstride, int T, int D, int tps,
+                    float* x_out, std::string& err) {
+  ProfScope prof_(c, "gate_residual");
+  gate_residual_kernel<<<gs((long)T * D / 4), 256, 0, c->stream>>>(x_in, y, gate, gstride, T, D, tps, x_out);
+  return check_launch("gate_residual", err);
+}
+
+int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, float* dy,
+               std::string& err) {
+  ProfScope prof_(c, "gate_bwd");
+  gate_bwd_kernel<<<gs((long)T * D / 4), 256, 0, c->stream>>>(gx, gate, gstride, T, D, tps, dy);
+  return check_launch("gate_bwd", err);
+}
+
+int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err) {
+  ProfScope prof_(c, "add");
+  add_kernel<<<gs(n), 256, 0, c->stream>>>(x, y, n, out);
+  return check_launch("add", err);
+}
+
+int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err) {
+  ProfScope prof_(c, "swiglu_fwd");
+  swiglu_fwd_kernel<<<gs((long)T * I), 256, 0, c->stream>>>(f, T, I, a);
+  return check_launch("swiglu_fwd", err);
+}
+
+int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err) {
+  ProfScope prof_(c, "swiglu_bwd");
+  swiglu_bwd_kernel<<<gs((long)T * I), 256, 0, c->stream>>>(da, f, T, I, df);
+  return check_launch("swiglu_bwd", err);
+}
+
+int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err) {
+  ProfScope prof_(c, "silu");
+  silu_bf16_kernel<<<gs(n), 256, 0, c->stream>>>(x, n, out);
+  return check_launch("silu", err);
+}
+
+int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err) {
+  ProfScope prof_(c, "modulation");
+  modulation_kernel<<<gs((long)B * 6 * D), 256, 0, c->stream>>>(ssg, gcond, B, D, mod);
+  return check_launch("modulation", err);
+}
+
+int k_mse(Ctx* c, const float* vel, const float* target, int B, long per, float* loss, float* dvel, std::string& err) {
+  ProfScope prof_(c, "mse");
+  if (cudaMemsetAsync(loss, 0, sizeof(float) * B, c->stream) != cudaSuccess) return check_launch("mse memset", err);
+  dim3 grid(16, (unsigned)B);
+  mse_kernel<<<grid, 256, 0, c->stream>>>(vel, target, per, 1.0f / (float)per, loss, dvel);
+  return check_launch("mse", err);
+}
+
+int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __nv_bfloat16* dst_bf,
+                int dst_rows_per, int dst_off, int B, int rows, int D, std::string& err) {
+  ProfScope prof_(c, "copy_rows");
+  copy_rows_kernel<<<gs((long)B * rows * D), 256, 0, c->stream>>>(src, src_rows_per, src_off, dst, dst_bf, dst_rows_per,
+                                                                  dst_off, B, rows, D);
+  return check_launch("copy_rows", err);
+}
+
+}  // namespace sa3k

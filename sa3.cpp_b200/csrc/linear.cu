@@ -1,0 +1,150 @@
+// linear.cu -- forward and backward of the adapted frozen-base linear over the tcgen05 engine.
+//
+// Forward (src/dit.h:106-147):
+//   u = x A^T                               rank-16 GEMM                      [M][16]
+//   y = g * (x W^T  (+)  (s u) B^T) + bias  one GEMM: the LoRA term is a K = 16 extension of the
+//                                           base MMA chain; g (DoRA) and bias in the epilogue
+// Backward (what ggml_build_backward_expand derives for those ops, src/train_ckpt.h:400):
+//   dz = g * dy,  dg = colsum(dy * (y - bias) / g)                  (prologue, dora)
+//   du = s dz B                                                     rank-16 GEMM
+//   dx = dz W  (+)  du A                                            one GEMM, K = 16 extension
+//   dB = s dz^T u,  dA = du^T x                                     skinny GEMMs (split-K)
+//   dora:  dm = dg / |.|,  dB += dt2 P + 2 dt3 (B A A^T),
+//          dA += (dt2 B)^T W + 2 (B^T diag(dt3) B) A                rank-16 quant GEMM + 16x16
+#include "linear.h"
+#include "lora_kernels.h"
+
+namespace sa3k {
+
+static size_t al(size_t b) { return (b + 255) & ~(size_t)255; }
+
+size_t adapter_prep_bytes(int64_t in, int64_t out, bool dora) {
+  size_t b = al(16 * in * 2) + al(in * 64 * 2) + al(out * 64 * 2) + al(16 * out * 2);
+  if (dora) b += al(16 * out * 4) + al(256 * 4) + al(out * 4) + al(out * 4);
+  return b;
+}
+
+void adapter_bind(AdapterPrep& p, void* mem) {
+  char* q = static_cast<char*>(mem);
+  auto take = [&](size_t bytes) { void* r = q; q += al(bytes); return r; };
+  p.a_bf = static_cast<__nv_bfloat16*>(take(16 * p.in * 2));
+  p.at_x = static_cast<__nv_bfloat16*>(take(p.in * 64 * 2));
+  p.b_x = static_cast<__nv_bfloat16*>(take(p.out * 64 * 2));
+  p.bt_bf = static_cast<__nv_bfloat16*>(take(16 * p.out * 2));
+  if (p.dora()) {
+    p.pt = static_cast<float*>(take(16 * p.out * 4));
+    p.aat = static_cast<float*>(take(256 * 4));
+    p.nsq = static_cast<float*>(take(p.out * 4));
+    p.g = static_cast<float*>(take(p.out * 4));
+  }
+}
+
+int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
+  if (k_prep_adapter(c, p.A, p.B, p.rank, p.in, p.out, p.a_bf, p.at_x, p.b_x, p.bt_bf, err)) return 1;
+  if (!p.dora()) return 0;
+  GemmDesc g;   // P^T = A W^T  [16][out]
+  g.M = 16; g.N = (int)p.out; g.K = (int)p.in;
+  g.a = p.a_bf; g.lda = p.in;
+  g.bsrc = kB_WEIGHT_NT; g.w = w;
+  g.out = p.pt; g.ldo = p.out;
+  g.name = "dora.P";
+  if (gemm(c, g, err)) return 1;
+  if (k_aat(c, p.A, p.rank, p.in, p.aat, err)) return 1;
+  return k_dora_norm(c, p.pt, p.B, p.rank, p.out, p.aat, p.bns, p.m, p.s, p.nsq, p.g, err);
+}
+
+int linear_forward(Ctx* c, const LinearFwd& f, std::string& err) {
+  const Weight* w = f.w;
+  const AdapterPrep* ad = f.ad;
+  if (ad) {
+    GemmDesc g;   // u = x A^T  [M][16]
+    g.M = (int)f.M; g.N = 16; g.K = (int)w->in;
+    g.a = f.x_bf; g.lda = w->in;
+    g.bsrc = kB_BF16_KMAJOR; g.b = ad->a_bf; g.ldb = w->in;
+    g.out = f.u; g.ldo = 16; g.bn = 16;
+    g.name = "lora.u";
+    if (gemm(c, g, err)) return 1;
+    if (k_pack_rank(c, f.u, (int)f.M, ad->s, f.ext_u, 1.0f, f.ut, (int)f.ut_ld, err)) return 1;
+  }
+  GemmDesc g;   // y = g * (x W^T + s u B^T) + bias
+  g.M = (int)f.M; g.N = (int)w->out; g.K = (int)w->in;
+  g.a = f.x_bf; g.lda = w->in;
+  g.bsrc = kB_WEIGHT_NT; g.w = w;
+  if (ad) { g.ext_a = f.ext_u; g.ext_b = ad->b_x; }
+  g.col_scale = (ad && ad->dora()) ? ad->g : nullptr;
+  g.col_bias = f.bias;
+  g.out = f.y; g.ldo = w->out;
+  g.out_bf = f.y_bf; g.ldo_bf = w->out;
+  g.name = "linear.fwd";
+  return gemm(c, g, err);
+}
+
+int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
+  const Weight* w = b.w;
+  const AdapterPrep* ad = b.ad;
+  const bool dora = ad && ad->dora();
+  const int64_t in = w->in, out = w->out;
+  const int rank = ad ? ad->rank : 0;
+  if (dora && cudaMemsetAsync(b.dg, 0, sizeof(float) * out, c->stream) != cudaSuccess)
+    return check_launch("memset", err);
+  if (k_bwd_prologue(c, b.dy, dora ? b.y : nullptr, b.bias, dora ? ad->g : nullptr, b.M, out, b.dz,
+                     dora ? b.dg : nullptr, err))
+    return 1;
+  if (ad) {
+    GemmDesc g;   // du = s dz B  [M][16]
+    g.M = (int)b.M; g.N = 16; g.K = (int)out;
+    g.a = b.dz; g.lda = out;
+    g.bsrc = kB_BF16_KMAJOR; g.b = ad->bt_bf; g.ldb = out;
+    g.alpha = ad->s;
+    g.out = b.du; g.ldo = 16; g.bn = 16;
+    g.name = "lora.du";
+    if (gemm(c, g, err)) return 1;
+    if (k_pack_rank(c, b.du, (int)b.M, 1.0f, b.ext_du, 1.0f, b.dut, (int)b.ut_ld, err)) return 1;
+  }
+  if (b.dx || b.dx_bf) {
+    GemmDesc g;   // dx = dz W + du A
+    g.M = (int)b.M; g.N = (int)in; g.K = (int)out;
+    g.a = b.dz; g.lda = out;
+    g.bsrc = kB_WEIGHT_TN; g.w = w;
+    if (ad) { g.ext_a = b.ext_du; g.ext_b = ad->at_x; }
+    g.out = b.dx; g.ldo = in; g.accumulate = b.dx_accumulate;
+    g.out_bf = b.dx_bf; g.ldo_bf = in;
+    g.name = "linear.dx";
+    if (gemm(c, g, err)) return 1;
+  }
+  if (!ad) return 0;
+  {
+    GemmDesc g;   // dB = s dz^T u  [out][rank]
+    g.M = (int)out; g.N = rank; g.K = (int)b.M;
+    g.a = b.dz; g.lda = out; g.a_mn = 1;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.ut; g.ldb = b.ut_ld;
+    g.alpha = ad->s;
+    g.out = b.dB; g.ldo = rank; g.accumulate = b.grad_accumulate; g.bn = 16;
+    g.name = "lora.dB";
+    if (gemm(c, g, err)) return 1;
+  }
+  {
+    GemmDesc g;   // dA = du^T x  [rank][in]
+    g.M = rank; g.N = (int)in; g.K = (int)b.M;
+    g.a = b.dut; g.lda = b.ut_ld;
+    g.bsrc = kB_BF16_MNMAJOR; g.b = b.x_bf; g.ldb = in;
+    g.out = b.dA; g.ldo = in; g.accumulate = b.grad_accumulate;
+    g.name = "lora.dA";
+    if (gemm(c, g, err)) return 1;
+  }
+  if (!dora) return 0;
+  if (cudaMemsetAsync(b.c3, 0, sizeof(float) * 256, c->stream) != cudaSuccess) return check_launch("memset", err);
+  if (k_dora_bwd(c, ad->pt, ad->B, rank, out, ad->aat, ad->nsq, ad->g, b.dg, ad->s, b.dm, b.grad_accumulate, b.dB,
+                 b.cb, b.c3, err))
+    return 1;
+  GemmDesc g;   // dA += (dt2 B)^T W
+  g.M = rank; g.N = (int)in; g.K = (int)out;
+  g.a = b.cb; g.lda = out;
+  g.bsrc = kB_WEIGHT_TN; g.w = w;
+  g.out = b.dA; g.ldo = in; g.accumulate = 1;
+  g.name = "dora.dA";
+  if (gemm(c, g, err)) return 1;
+  return k_dora_da_c3(c, b.c3, ad->A, rank, in, b.dA, err);
+}
+
+}  // namespace sa3k

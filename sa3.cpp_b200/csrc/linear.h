@@ -1,0 +1,80 @@
+// linear.h -- the adapted frozen-base linear (dit_lin, src/dit.h:92-149) as a reusable engine.
+#pragma once
+
+#include "sa3k_internal.h"
+
+namespace sa3k {
+
+// Per-step derived forms of one LoRA / DoRA-rows adapter.  The buffers are owned by the caller;
+// adapter_prepare() fills them from A, B (and for DoRA m, base_norm_sq) once per optimizer step,
+// and every forward / backward of that step reuses them.
+struct AdapterPrep {
+  int rank = 0;
+  int64_t in = 0, out = 0;
+  float s = 1.0f;                      // alpha / rank
+  const float* A = nullptr;            // [rank][in]
+  const float* B = nullptr;            // [out][rank]
+  const float* m = nullptr;            // [out] dora-rows magnitude (null: plain LoRA)
+  const float* bns = nullptr;          // [out] base row norm^2 + in*eps
+  __nv_bfloat16* a_bf = nullptr;       // [16][in]
+  __nv_bfloat16* at_x = nullptr;       // [in][64]  A^T, extension operand of dx
+  __nv_bfloat16* b_x = nullptr;        // [out][64] B, extension operand of y
+  __nv_bfloat16* bt_bf = nullptr;      // [16][out] B^T
+  float* pt = nullptr;                 // [16][out] (W A^T)^T          (dora)
+  float* aat = nullptr;                // [16][16]                      (dora)
+  float* nsq = nullptr;                // [out] |W + s B A|_row^2       (dora)
+  float* g = nullptr;                  // [out] m / sqrt(nsq)           (dora)
+  bool dora() const { return m != nullptr; }
+};
+
+// bytes of device scratch one AdapterPrep needs (dora or not), laid out by adapter_bind()
+size_t adapter_prep_bytes(int64_t in, int64_t out, bool dora);
+void adapter_bind(AdapterPrep& p, void* mem);
+int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err);
+
+struct LinearFwd {
+  const Weight* w = nullptr;
+  const AdapterPrep* ad = nullptr;     // null: plain mul_mat
+  const float* bias = nullptr;
+  const __nv_bfloat16* x_bf = nullptr; // [M][in] bf16 input
+  int64_t M = 0;
+  float* y = nullptr;                  // [M][out] f32 output (nullable)
+  __nv_bfloat16* y_bf = nullptr;       // [M][out] bf16 output (nullable)
+  // adapter scratch: u [M][16] f32, ext_u [M][64] bf16, ut [16][ut_ld] bf16 (kept for backward)
+  float* u = nullptr;
+  __nv_bfloat16* ext_u = nullptr;
+  __nv_bfloat16* ut = nullptr;
+  int64_t ut_ld = 0;
+};
+int linear_forward(Ctx* c, const LinearFwd& f, std::string& err);
+
+struct LinearBwd {
+  const Weight* w = nullptr;
+  const AdapterPrep* ad = nullptr;
+  const float* bias = nullptr;
+  const __nv_bfloat16* x_bf = nullptr; // forward input [M][in]
+  const float* y = nullptr;            // forward output [M][out] (needed by dora-rows)
+  const float* dy = nullptr;           // upstream gradient [M][out] f32
+  int64_t M = 0;
+  const __nv_bfloat16* ut = nullptr;   // u^T from the forward [16][ut_ld] (adapter)
+  int64_t ut_ld = 0;
+  float* dx = nullptr;                 // [M][in] f32 (nullable)
+  int dx_accumulate = 0;
+  __nv_bfloat16* dx_bf = nullptr;      // [M][in] bf16 (nullable; not with dx_accumulate)
+  float* dA = nullptr;                 // [rank][in]
+  float* dB = nullptr;                 // [out][rank]
+  float* dm = nullptr;                 // [out] (dora)
+  int grad_accumulate = 0;
+  // scratch: dz [M][out] bf16, dg [out], du [M][16], ext_du [M][64] bf16, dut [16][ut_ld] bf16,
+  // cb [16][out] bf16, c3 [256]
+  __nv_bfloat16* dz = nullptr;
+  float* dg = nullptr;
+  float* du = nullptr;
+  __nv_bfloat16* ext_du = nullptr;
+  __nv_bfloat16* dut = nullptr;
+  __nv_bfloat16* cb = nullptr;
+  float* c3 = nullptr;
+};
+int linear_backward(Ctx* c, const LinearBwd& b, std::string& err);
+
+}  // namespace sa3k

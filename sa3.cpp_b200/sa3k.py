@@ -20,6 +20,7 @@ ABI_SYMBOLS = (
     "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_linear_fwd",
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
+    "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N = 1, 2, 3
 
@@ -31,6 +32,19 @@ class Sa3kError(RuntimeError):
 class Adapter(ctypes.Structure):
     _fields_ = [("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("magnitude", ctypes.c_void_p),
                 ("base_norm_sq", ctypes.c_void_p), ("scale", ctypes.c_float), ("rank", ctypes.c_int)]
+
+
+class Tensor4(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("batch_stride", ctypes.c_int64), ("head_stride", ctypes.c_int64),
+                ("row_stride", ctypes.c_int64)]
+
+
+class HeadSliceC(ctypes.Structure):
+    _fields_ = [("col", ctypes.c_int), ("gamma", ctypes.c_void_p), ("rope", ctypes.c_int), ("rstd", ctypes.c_void_p)]
+
+
+def t4(t, batch_stride, head_stride, row_stride):
+    return Tensor4(ctypes.c_void_p(t.data_ptr()), batch_stride, head_stride, row_stride)
 
 
 class ProfileEntry(ctypes.Structure):
@@ -72,6 +86,11 @@ def lib():
                                               ctypes.POINTER(ctypes.c_double), E, I]
         L.sa3k_profile_enable.argtypes = [P, I, E, I]
         L.sa3k_ctx_set_option.argtypes = [P, I, I64, E, I]
+        T4 = ctypes.POINTER(Tensor4)
+        L.sa3k_attention_fwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, P, E, I]
+        L.sa3k_attention_bwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, T4, P, T4, T4, T4, E, I]
+        L.sa3k_head_prep_fwd.argtypes = [P, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, I, F, P, E, I]
+        L.sa3k_head_prep_bwd.argtypes = [P, P, I64, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, P, E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
             if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free"):
@@ -143,6 +162,30 @@ class Context:
         arr = (ProfileEntry * max(n.value, 1))()
         _check(lib().sa3k_profile_read(self._h, arr, n.value, ctypes.byref(n), err, 256), err)
         return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(n.value)}
+
+    # -------------------------------------------------------------------- attention
+    def attention_fwd(self, B, H, Sq, Sk, scale, window, q, k, v, o, lse):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_attention_fwd(self._h, B, H, Sq, Sk, 64, scale, window, ctypes.byref(q), ctypes.byref(k),
+                                        ctypes.byref(v), ctypes.byref(o), _ptr(lse), err, 512), err)
+
+    def attention_bwd(self, B, H, Sq, Sk, scale, window, q, k, v, o, dO, lse, dq, dk=None, dv=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_attention_bwd(self._h, B, H, Sq, Sk, 64, scale, window, ctypes.byref(q), ctypes.byref(k),
+                                        ctypes.byref(v), ctypes.byref(o), ctypes.byref(dO), _ptr(lse), ctypes.byref(dq),
+                                        ctypes.byref(dk) if dk else None, ctypes.byref(dv) if dv else None, err, 512),
+               err)
+
+    def head_prep_fwd(self, y, T, ncols, H, slices, tps, eps, rot, base, out):
+        err = ctypes.create_string_buffer(512)
+        arr = (HeadSliceC * len(slices))(*slices)
+        _check(lib().sa3k_head_prep_fwd(self._h, _ptr(y), T, ncols, H, arr, len(slices), tps, eps, rot, base, _ptr(out),
+                                        err, 512), err)
+
+    def head_prep_bwd(self, g, g_ld, y, T, ncols, H, sl, tps, rot, base, dy):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_head_prep_bwd(self._h, _ptr(g), g_ld, _ptr(y), T, ncols, H, ctypes.byref(sl), tps, rot, base,
+                                        _ptr(dy), err, 512), err)
 
     # -------------------------------------------------------------------- weights
     def upload(self, raw_bytes, qtype, inn, out):
