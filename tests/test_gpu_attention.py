@@ -179,8 +179,9 @@ def test_config3_banded_rope_attention(ctx):
     vh = x[:, :, 2]
     tr = lambda t: t.permute(0, 2, 1, 3)
     # the kernel consumes the bf16-rounded roped q / k; round the reference the same way
-    qr = tr(qh).to(torch.bfloat16).double() + (tr(qh) - tr(qh).detach())
-    kr = tr(kh).to(torch.bfloat16).double() + (tr(kh) - tr(kh).detach())
+    # (straight-through: the rounded value forward, the identity backward)
+    qr = tr(qh).detach().to(torch.bfloat16).double() + (tr(qh) - tr(qh).detach())
+    kr = tr(kh).detach().to(torch.bfloat16).double() + (tr(kh) - tr(kh).detach())
     ref_o = oracle.sdpa(qr, kr, tr(vh), 0.125, W)
     dOr = dO.double().reshape(B, S, H, 64)[:, :, heads].permute(0, 2, 1, 3)
     ref_o.backward(dOr)
