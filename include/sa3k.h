@@ -212,6 +212,71 @@ int sa3k_average_clip_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, f
                             int64_t n, int count, const sa3k_adamw_params* hp, int step,
                             double* grad_norm_out, char* err, int err_len);
 
+/* ------------------------------------------------------------------ the DiT training step */
+
+/* DiT hyper-parameters, as DitConfig (src/dit.h:20-47) plus the SwiGLU inner width. */
+typedef struct sa3k_dit_config {
+  int io, dim, depth, heads, head_dim, cond_dim, mem_tokens, rot, time_dim, ff_inner, differential;
+  float rope_base, norm_eps, qk_eps, time_min_freq, time_max_freq;
+} sa3k_dit_config;
+
+typedef struct sa3k_dit sa3k_dit;
+
+/* A DiT bound to a context.  Replaces building the training graphs, build_train_dit_ckpt
+ * (src/train_ckpt.h:143-474); the model keeps its activations resident, so no recompute. */
+int sa3k_dit_create(sa3k_ctx* ctx, const sa3k_dit_config* cfg, sa3k_dit** out, char* err,
+                    int err_len);
+void sa3k_dit_free(sa3k_dit* dit);
+
+/* Set one GGUF tensor by its name (the names dit.h reads, e.g. "dit.3.self.qkv.weight",
+ * "dit.3.pre_norm.gamma", "dit.memory_tokens").  *.weight tensors may be F32 / F16 / Q8_0 / Q4_K
+ * row bytes [ne1 = out][ne0 = in]; every other tensor is F32.  Replaces GgufModel loading
+ * (src/gguf_model.h:280-331). */
+int sa3k_dit_set_tensor(sa3k_dit* dit, const char* name, int ggml_type, const void* host,
+                        int64_t ne0, int64_t ne1, char* err, int err_len);
+
+/* Functional adapters ("lora" or "dora-rows", rank <= 16) on the named per-block weights.
+ * Allocates the flat adapter state [A | B | m] per target (order of `names`), zero; for
+ * dora-rows computes base_norm_sq and initialises m to the base row norms (src/train_lora.h:
+ * 141-174, 262-263).  A and B are then written by the caller through sa3k_dit_adapter_buffer.
+ * Counterpart of init_train_lora_state (src/train_lora.h:205-273) for the device state. */
+int sa3k_dit_init_adapters(sa3k_dit* dit, const char* adapter_type, int rank, float alpha,
+                           const char* const* names, int n, char* err, int err_len);
+
+/* Total floats of the flat adapter state and the offsets of target idx in it (offM = -1 for
+ * plain LoRA). */
+int64_t sa3k_dit_adapter_size(const sa3k_dit* dit);
+int sa3k_dit_adapter_offsets(const sa3k_dit* dit, int idx, int64_t* offA, int64_t* offB,
+                             int64_t* offM);
+
+/* Device pointer of a flat buffer: 0 parameters, 1 accumulated gradients, 2 AdamW m, 3 AdamW v
+ * (TrainLoraState / TrainLoraGradAccum / TrainLoopState of src/train_loop.h:21-39). */
+int sa3k_dit_adapter_buffer(sa3k_dit* dit, int which, float** dev_ptr, char* err, int err_len);
+
+/* Copy `count` floats at `offset` of flat buffer `which` (as above) from buf into the model
+ * (to_model != 0) or out of it into buf; buf may be host or device memory.  Synchronous.
+ * Counterpart of upload_train_lora_state / train_read_grad (src/train_loop.h:41-73). */
+int sa3k_dit_adapter_copy(sa3k_dit* dit, int which, float* buf, int64_t offset, int64_t count,
+                          int to_model, char* err, int err_len);
+
+/* Zero the accumulated gradients (train_clear_accum, src/train_loop.h:80-82). */
+int sa3k_dit_zero_grads(sa3k_dit* dit, char* err, int err_len);
+
+/* Forward + backward of B samples of T frames: x_t, target [B][T][io]; t_feat [B][time_dim]
+ * (expo_features, src/sa3_pipeline.h:57-67); cross [B][ctx_len][cond_dim]; global [B][cond_dim]
+ * (host or device pointers).  Adds the adapter gradients of the summed per-sample losses to the
+ * accumulated gradients and writes the B per-sample losses (mean squared error over io*T) to
+ * `loss` (host or device, nullable).  Replaces run_train_dit_accumulate_ckpt
+ * (src/train_loop.h:309-441) called once per sample. */
+int sa3k_dit_forward_backward(sa3k_dit* dit, int B, int T, int ctx_len, const float* x_t,
+                              const float* target, const float* t_feat, const float* cross,
+                              const float* global, float* loss, char* err, int err_len);
+
+/* Average over `count` samples, clip, AdamW (train_apply_accumulated_adamw,
+ * src/train_loop.h:173-211) on the flat state. */
+int sa3k_dit_apply_adamw(sa3k_dit* dit, int count, const sa3k_adamw_params* hp, int step,
+                         double* grad_norm_out, char* err, int err_len);
+
 #ifdef __cplusplus
 }
 #endif

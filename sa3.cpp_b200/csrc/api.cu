@@ -11,13 +11,6 @@
 #include <cstring>
 #include <new>
 
-struct sa3k_ctx {
-  sa3k::Ctx c;
-};
-struct sa3k_weight {
-  sa3k::Weight w;
-};
-
 namespace sa3k {
 
 static int fill_err(char* err, int len, const std::string& msg) {

@@ -1,0 +1,632 @@
+// dit.cu -- the DiT adapter-training step on one GPU: forward through the frozen (quantized)
+// DiT with functional LoRA / DoRA-rows adapters, MSE v-objective loss, full backward to the
+// adapter gradients, and the averaged + clipped AdamW update.
+//
+// Reference: dit_head / dit_block / dit_tail (src/dit.h:164-323) built into training graphs by
+// build_train_dit_ckpt (src/train_ckpt.h:143-474) and run per sample by
+// run_train_dit_accumulate_ckpt (src/train_loop.h:309-441); the update is
+// train_apply_accumulated_adamw (src/train_loop.h:173-211).
+//
+// Differences of execution (not of math):
+//  * a batch of B samples runs as one pass: every linear sees M = B * (mem + T) token rows, the
+//    per-sample pieces (adaLN vectors, attention, positions, loss) are indexed by sample; the
+//    adapter gradients are the sum over samples, as the reference's host accumulation.
+//  * all activations stay resident in HBM (about 0.6 GB per block at batch 4, medium width), so
+//    the backward does not recompute the forward; the reference's checkpointed VJP
+//    (src/train_ckpt.h:12-18) is the same gradient.
+//  * adapters live in one flat f32 buffer [A | B | m] per target, gradients and moments alike;
+//    the A/B operand packing and the DoRA norms are prepared once per step.
+//  * head adapters are not supported (the reference skips the head graph when none exist,
+//    src/train_ckpt.h:292-317); targets must be per-block projections.
+#include "../../include/sa3k.h"
+#include "attention.h"
+#include "linear.h"
+#include "lora_kernels.h"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+namespace sa3k {
+
+struct DitTarget {
+  std::string name;
+  const Weight* w = nullptr;
+  int64_t in = 0, out = 0;
+  int64_t offA = 0, offB = 0, offM = -1;   // into the flat adapter state
+  float* bns = nullptr;                    // [out]
+  AdapterPrep prep;
+};
+
+struct DitBlockAct {
+  float *x = nullptr, *rstd_a = nullptr, *qkv = nullptr, *rq = nullptr, *rk = nullptr, *lse_a = nullptr;
+  float *yo = nullptr, *x1 = nullptr, *rstd_c = nullptr, *qf = nullptr, *rcq = nullptr, *kvf = nullptr;
+  float *rck = nullptr, *lse_c = nullptr, *x2 = nullptr, *rstd_f = nullptr, *ff = nullptr, *yf = nullptr;
+  float* mod = nullptr;
+  __nv_bfloat16 *h_a = nullptr, *qkvb = nullptr, *oa = nullptr, *hc = nullptr, *cq = nullptr, *kvb = nullptr;
+  __nv_bfloat16 *oc = nullptr, *hf = nullptr, *act = nullptr;
+  __nv_bfloat16* ut[4] = {nullptr, nullptr, nullptr, nullptr};
+};
+
+struct DitModel {
+  Ctx* c = nullptr;
+  sa3k_ctx* handle = nullptr;
+  sa3k_dit_config cfg{};
+  std::map<std::string, Weight*> W;
+  std::vector<sa3k_weight*> weights;   // owned weight handles (W points into them)
+  std::map<std::string, float*> V;
+  std::vector<void*> owned;            // device allocations of this model
+  // adapters
+  bool dora = false;
+  int rank = 0;
+  float alpha = 1.f, s = 1.f;
+  std::vector<DitTarget> tg;
+  std::map<std::string, int> tix;
+  float *p = nullptr, *g = nullptr, *am = nullptr, *av = nullptr;
+  int64_t np = 0;
+  void* prep_mem = nullptr;
+  // activations for shape (B, T, C)
+  int B = 0, T = 0, C = 0;
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<DitBlockAct> blk;
+  float* x_final = nullptr;
+  // inputs
+  float *in_x = nullptr, *in_target = nullptr, *in_tfeat = nullptr, *in_cross = nullptr, *in_glob = nullptr;
+  // head
+  float *te_h = nullptr, *te = nullptr, *g_h = nullptr, *gsum = nullptr, *gce_h = nullptr, *gcond = nullptr;
+  float *ctx_h = nullptr, *pre = nullptr, *xin0 = nullptr;
+  __nv_bfloat16 *tfeat_b = nullptr, *te_hb = nullptr, *glob_b = nullptr, *g_hb = nullptr, *gsum_b = nullptr;
+  __nv_bfloat16 *gce_hb = nullptr, *cross_b = nullptr, *ctx_hb = nullptr, *context_b = nullptr, *xt_b = nullptr;
+  __nv_bfloat16* xp_b = nullptr;
+  // tail
+  __nv_bfloat16 *xT_b = nullptr, *pout_b = nullptr;
+  float *pout = nullptr, *vel = nullptr, *dvel = nullptr, *loss = nullptr, *dp = nullptr, *dxT = nullptr;
+  // backward temporaries
+  float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dact = nullptr, *dq3 = nullptr, *Dsum = nullptr;
+  __nv_bfloat16* dO_b = nullptr;
+  // linear scratch
+  float *u = nullptr, *du = nullptr, *dg = nullptr, *c3 = nullptr;
+  __nv_bfloat16 *ext_u = nullptr, *ext_du = nullptr, *dut = nullptr, *dz = nullptr, *cb = nullptr;
+  int64_t ut_ld = 0;
+
+  ~DitModel() {
+    for (void* q : owned) cudaFree(q);
+    if (arena) cudaFree(arena);
+    for (sa3k_weight* h : weights) sa3k_weight_free(h);
+  }
+
+  int Sfull() const { return cfg.mem_tokens + T; }
+  int qkv_cols() const { return (cfg.differential ? 5 : 3) * cfg.dim; }
+  std::string bname(int l, const char* suffix) const { return "dit." + std::to_string(l) + "." + suffix; }
+  const Weight* weight(const std::string& n, std::string& err) const {
+    auto it = W.find(n);
+    if (it == W.end()) { err = "missing weight " + n; return nullptr; }
+    return it->second;
+  }
+  const float* vec(const std::string& n, std::string& err) const {
+    auto it = V.find(n);
+    if (it == V.end()) { err = "missing tensor " + n; return nullptr; }
+    return it->second;
+  }
+};
+
+static void* dmalloc(DitModel& m, size_t bytes, std::string& err) {
+  void* q = nullptr;
+  if (cudaMalloc(&q, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    err = "out of device memory";
+    return nullptr;
+  }
+  m.owned.push_back(q);
+  return q;
+}
+
+// ------------------------------------------------------------------ activation arena
+static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
+  if (m.arena && m.B == B && m.T == T && m.C == C) return 0;
+  if (m.arena) { cudaStreamSynchronize(m.c->stream); cudaFree(m.arena); m.arena = nullptr; }
+  const sa3k_dit_config& k = m.cfg;
+  m.B = B; m.T = T; m.C = C;
+  const int64_t S = m.Sfull(), M = (int64_t)B * S, D = k.dim, Hh = k.heads, I = k.ff_inner;
+  const int64_t Q = m.qkv_cols(), MC = (int64_t)B * C, MT = (int64_t)B * T;
+  m.ut_ld = (M + 63) / 64 * 64;
+  // two passes: measure, then carve
+  for (int pass = 0; pass < 2; ++pass) {
+    char* base = static_cast<char*>(m.arena);
+    size_t off = 0;
+    auto take = [&](size_t bytes) -> void* {
+      void* r = pass ? base + off : nullptr;
+      off += (bytes + 255) & ~(size_t)255;
+      return r;
+    };
+    auto f = [&](int64_t n) { return static_cast<float*>(take(n * 4)); };
+    auto h = [&](int64_t n) { return static_cast<__nv_bfloat16*>(take(n * 2)); };
+    m.blk.assign(k.depth, DitBlockAct{});
+    for (int l = 0; l < k.depth; ++l) {
+      DitBlockAct& a = m.blk[l];
+      a.x = f(M * D); a.rstd_a = f(M); a.h_a = h(M * D); a.qkv = f(M * Q); a.qkvb = h(M * Q);
+      a.rq = f(M * Hh); a.rk = f(M * Hh); a.oa = h(M * D); a.lse_a = f(B * Hh * S); a.yo = f(M * D);
+      a.x1 = f(M * D); a.rstd_c = f(M); a.hc = h(M * D); a.qf = f(M * D); a.cq = h(M * D); a.rcq = f(M * Hh);
+      a.kvf = f(MC * 2 * D); a.kvb = h(MC * 2 * D); a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
+      a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = f(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
+      a.mod = f(B * 6 * D);
+      for (int j = 0; j < 4; ++j) a.ut[j] = h(16 * m.ut_ld);
+    }
+    m.x_final = f(M * D);
+    m.in_x = f(MT * k.io); m.in_target = f(MT * k.io); m.in_tfeat = f(B * k.time_dim);
+    m.in_cross = f(MC * k.cond_dim); m.in_glob = f(B * k.cond_dim);
+    m.te_h = f(B * D); m.te = f(B * D); m.g_h = f(B * D); m.gsum = f(B * D); m.gce_h = f(B * D); m.gcond = f(B * 6 * D);
+    m.ctx_h = f(MC * D); m.pre = f(MT * k.io); m.xin0 = f(MT * D);
+    m.tfeat_b = h(B * k.time_dim); m.te_hb = h(B * D); m.glob_b = h(B * k.cond_dim); m.g_hb = h(B * D);
+    m.gsum_b = h(B * D); m.gce_hb = h(B * D); m.cross_b = h(MC * k.cond_dim); m.ctx_hb = h(MC * D);
+    m.context_b = h(MC * D); m.xt_b = h(MT * k.io); m.xp_b = h(MT * k.io);
+    m.xT_b = h(MT * D); m.pout_b = h(MT * k.io); m.pout = f(MT * k.io); m.vel = f(MT * k.io); m.dvel = f(MT * k.io);
+    m.loss = f(64); m.dp = f(MT * k.io); m.dxT = f(MT * D);
+    const int64_t wide = std::max<int64_t>(std::max<int64_t>(Q, 2 * I), D);
+    m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact = f(M * I); m.dq3 = f(M * Q);
+    m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
+    const int64_t maxout = std::max<int64_t>(wide, 6 * D);
+    m.u = f(M * 16); m.du = f(M * 16); m.dg = f(maxout); m.c3 = f(256);
+    m.ext_u = h(M * 64); m.ext_du = h(M * 64); m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
+    if (pass == 0) {
+      m.arena_bytes = off;
+      if (cudaMalloc(&m.arena, off) != cudaSuccess) {
+        cudaGetLastError();
+        err = "out of device memory for DiT activations (" + std::to_string(off >> 20) + " MiB)";
+        m.arena = nullptr;
+        return 1;
+      }
+    }
+  }
+  return 0;
+}
+
+// ------------------------------------------------------------------ linear helpers
+static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __nv_bfloat16* x,
+                   int64_t M, float* y, __nv_bfloat16* y_bf, __nv_bfloat16* ut, std::string& err) {
+  LinearFwd f;
+  f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_bf = x; f.M = M; f.y = y; f.y_bf = y_bf;
+  f.u = m.u; f.ext_u = m.ext_u; f.ut = ut; f.ut_ld = m.ut_ld;
+  return linear_forward(m.c, f, err);
+}
+
+static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
+                   const float* y, const float* dy, int64_t M, const __nv_bfloat16* ut, float* dx, int dx_acc,
+                   __nv_bfloat16* dx_bf, std::string& err) {
+  LinearBwd b;
+  b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;
+  b.ut = ut; b.ut_ld = m.ut_ld; b.dx = dx; b.dx_accumulate = dx_acc; b.dx_bf = dx_bf;
+  if (t) {
+    b.dA = m.g + t->offA; b.dB = m.g + t->offB; b.dm = t->offM >= 0 ? m.g + t->offM : nullptr;
+    b.grad_accumulate = 1;
+  }
+  b.dz = m.dz; b.dg = m.dg; b.du = m.du; b.ext_du = m.ext_du; b.dut = m.dut; b.cb = m.cb; b.c3 = m.c3;
+  return linear_backward(m.c, b, err);
+}
+
+// plain frozen MLP of dit_head: y = W2 silu(W1 x + b1) + b2 (src/dit.h:269-274)
+static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_bfloat16* x, int64_t M, float* h,
+                    __nv_bfloat16* hb, float* y, __nv_bfloat16* y_bf, std::string& err) {
+  const Weight* w0 = m.weight(pfx + "0.weight", err);
+  const Weight* w2 = m.weight(pfx + "2.weight", err);
+  if (!w0 || !w2) return 1;
+  const float* b0 = bias ? m.vec(pfx + "0.bias", err) : nullptr;
+  const float* b2 = bias ? m.vec(pfx + "2.bias", err) : nullptr;
+  if (bias && (!b0 || !b2)) return 1;
+  if (lin_fwd(m, w0, nullptr, b0, x, M, h, nullptr, nullptr, err)) return 1;
+  if (k_silu_bf16(m.c, h, M * w0->out, hb, err)) return 1;
+  return lin_fwd(m, w2, nullptr, b2, hb, M, y, y_bf, nullptr, err);
+}
+
+static DitTarget* target(DitModel& m, const std::string& name) {
+  auto it = m.tix.find(name);
+  return it == m.tix.end() ? nullptr : &m.tg[(size_t)it->second];
+}
+
+// ------------------------------------------------------------------ forward + backward
+static int dit_step(DitModel& m, std::string& err) {
+  Ctx* c = m.c;
+  const sa3k_dit_config& k = m.cfg;
+  const int B = m.B, T = m.T, C = m.C, S = m.Sfull(), D = k.dim, H = k.heads, I = k.ff_inner;
+  const int64_t M = (int64_t)B * S, MT = (int64_t)B * T, MC = (int64_t)B * C;
+  const int Q = m.qkv_cols();
+  const float scale = 1.0f / std::sqrt((float)k.head_dim);
+  if (k.differential) { err = "differential attention is not supported by the training step yet"; return 1; }
+
+  // adapters: operand forms + DoRA norms, once per step
+  for (DitTarget& t : m.tg)
+    if (adapter_prepare(c, t.w, t.prep, err)) return 1;
+
+  // ---------------- head (src/dit.h:286-310)
+  if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
+  if (mlp_silu(m, "dit.time_embed.", true, m.tfeat_b, B, m.te_h, m.te_hb, m.te, nullptr, err)) return 1;
+  if (k_cvt_bf16(c, m.in_glob, (int64_t)B * k.cond_dim, m.glob_b, err)) return 1;
+  if (mlp_silu(m, "dit.global_embed.", false, m.glob_b, B, m.g_h, m.g_hb, m.gsum, nullptr, err)) return 1;
+  if (k_add(c, m.gsum, m.te, (long)B * D, m.gsum, err)) return 1;
+  if (k_cvt_bf16(c, m.gsum, (int64_t)B * D, m.gsum_b, err)) return 1;
+  if (mlp_silu(m, "dit.gce.", true, m.gsum_b, B, m.gce_h, m.gce_hb, m.gcond, nullptr, err)) return 1;
+  if (k_cvt_bf16(c, m.in_cross, MC * k.cond_dim, m.cross_b, err)) return 1;
+  if (mlp_silu(m, "dit.cond_embed.", false, m.cross_b, MC, m.ctx_h, m.ctx_hb, nullptr, m.context_b, err)) return 1;
+  {
+    const Weight* wpre = m.weight("dit.pre_conv.weight", err);
+    const Weight* win = m.weight("dit.proj_in.weight", err);
+    const float* mem = m.vec("dit.memory_tokens", err);
+    if (!wpre || !win || !mem) return 1;
+    if (k_cvt_bf16(c, m.in_x, MT * k.io, m.xt_b, err)) return 1;
+    if (lin_fwd(m, wpre, nullptr, nullptr, m.xt_b, MT, m.pre, nullptr, nullptr, err)) return 1;
+    if (k_add(c, m.pre, m.in_x, (long)MT * k.io, m.pre, err)) return 1;
+    if (k_cvt_bf16(c, m.pre, MT * k.io, m.xp_b, err)) return 1;
+    if (lin_fwd(m, win, nullptr, nullptr, m.xp_b, MT, m.xin0, nullptr, nullptr, err)) return 1;
+    float* x0 = m.blk[0].x;
+    if (k_copy_rows(c, mem, 0, 0, x0, nullptr, S, 0, B, k.mem_tokens, D, err)) return 1;
+    if (k_copy_rows(c, m.xin0, T, 0, x0, nullptr, S, k.mem_tokens, B, T, D, err)) return 1;
+  }
+
+  // ---------------- blocks (src/dit.h:164-266)
+  for (int l = 0; l < k.depth; ++l) {
+    DitBlockAct& a = m.blk[l];
+    float* x_next = l + 1 < k.depth ? m.blk[l + 1].x : m.x_final;
+    const Weight *wqkv = m.weight(m.bname(l, "self.qkv.weight"), err), *wout = m.weight(m.bname(l, "self.out.weight"), err);
+    const Weight *wcq = m.weight(m.bname(l, "cross.q.weight"), err), *wckv = m.weight(m.bname(l, "cross.kv.weight"), err);
+    const Weight *wco = m.weight(m.bname(l, "cross.out.weight"), err), *wfp = m.weight(m.bname(l, "ff.proj.weight"), err);
+    const Weight* wfo = m.weight(m.bname(l, "ff.out.weight"), err);
+    const float *ssg = m.vec(m.bname(l, "ssg"), err), *g_pre = m.vec(m.bname(l, "pre_norm.gamma"), err);
+    const float *g_q = m.vec(m.bname(l, "self.q_norm.gamma"), err), *g_k = m.vec(m.bname(l, "self.k_norm.gamma"), err);
+    const float *g_cn = m.vec(m.bname(l, "cross_norm.gamma"), err), *g_cq = m.vec(m.bname(l, "cross.q_norm.gamma"), err);
+    const float *g_ck = m.vec(m.bname(l, "cross.k_norm.gamma"), err), *g_ff = m.vec(m.bname(l, "ff_norm.gamma"), err);
+    const float *b_fp = m.vec(m.bname(l, "ff.proj.bias"), err), *b_fo = m.vec(m.bname(l, "ff.out.bias"), err);
+    if (!wqkv || !wout || !wcq || !wckv || !wco || !wfp || !wfo || !ssg || !g_pre || !g_q || !g_k || !g_cn || !g_cq ||
+        !g_ck || !g_ff || !b_fp || !b_fo)
+      return 1;
+    DitTarget *tq = target(m, m.bname(l, "self.qkv.weight")), *to = target(m, m.bname(l, "self.out.weight"));
+    DitTarget *tp = target(m, m.bname(l, "ff.proj.weight")), *tf = target(m, m.bname(l, "ff.out.weight"));
+    if (target(m, m.bname(l, "cross.q.weight")) || target(m, m.bname(l, "cross.kv.weight")) ||
+        target(m, m.bname(l, "cross.out.weight"))) {
+      err = "adapters on cross-attention projections are not supported by the training step yet";
+      return 1;
+    }
+    const long ms = 6L * D;
+    if (k_modulation(c, ssg, m.gcond, B, D, a.mod, err)) return 1;
+    // self-attention branch
+    if (k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err)) return 1;
+    if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, a.ut[0], err)) return 1;
+    {
+      HeadSlice hs[3];
+      hs[0].col = 0; hs[0].gamma = g_q; hs[0].rope = 1; hs[0].rstd = a.rq;
+      hs[1].col = D; hs[1].gamma = g_k; hs[1].rope = 1; hs[1].rstd = a.rk;
+      hs[2].col = 2 * D;
+      if (k_head_prep_fwd(c, a.qkv, (int)M, Q, H, hs, 3, S, k.qk_eps, k.rot, k.rope_base, a.qkvb, err)) return 1;
+    }
+    AttnArgs sa;
+    sa.B = B; sa.H = H; sa.Sq = S; sa.Sk = S; sa.scale = scale; sa.window = -1;
+    sa.q = a.qkvb; sa.q_sb = (long)S * Q; sa.q_sh = 64; sa.q_ld = Q;
+    sa.k = a.qkvb + D; sa.k_sb = sa.q_sb; sa.k_sh = 64; sa.k_ld = Q;
+    sa.v = a.qkvb + 2 * D; sa.v_sb = sa.q_sb; sa.v_sh = 64; sa.v_ld = Q;
+    sa.o = a.oa; sa.o_sb = (long)S * D; sa.o_sh = 64; sa.o_ld = D;
+    sa.lse = a.lse_a;
+    if (attn_forward(c, sa, err)) return 1;
+    if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, a.ut[1], err)) return 1;
+    if (k_gate_residual(c, a.x, a.yo, a.mod + 2 * D, ms, (int)M, D, S, a.x1, err)) return 1;
+    // cross-attention branch
+    if (k_rmsnorm_mod_fwd(c, a.x1, (int)M, D, g_cn, nullptr, nullptr, 0, S, k.norm_eps, a.hc, a.rstd_c, err)) return 1;
+    if (lin_fwd(m, wcq, nullptr, nullptr, a.hc, M, a.qf, nullptr, nullptr, err)) return 1;
+    {
+      HeadSlice hs;
+      hs.col = 0; hs.gamma = g_cq; hs.rstd = a.rcq;
+      if (k_head_prep_fwd(c, a.qf, (int)M, D, H, &hs, 1, S, k.qk_eps, k.rot, k.rope_base, a.cq, err)) return 1;
+    }
+    if (lin_fwd(m, wckv, nullptr, nullptr, m.context_b, MC, a.kvf, nullptr, nullptr, err)) return 1;
+    {
+      HeadSlice hs[2];
+      hs[0].col = 0; hs[0].gamma = g_ck; hs[0].rstd = a.rck;
+      hs[1].col = D;
+      if (k_head_prep_fwd(c, a.kvf, (int)MC, 2 * D, H, hs, 2, C, k.qk_eps, k.rot, k.rope_base, a.kvb, err)) return 1;
+    }
+    AttnArgs ca;
+    ca.B = B; ca.H = H; ca.Sq = S; ca.Sk = C; ca.scale = scale; ca.window = -1;
+    ca.q = a.cq; ca.q_sb = (long)S * D; ca.q_sh = 64; ca.q_ld = D;
+    ca.k = a.kvb; ca.k_sb = (long)C * 2 * D; ca.k_sh = 64; ca.k_ld = 2 * D;
+    ca.v = a.kvb + D; ca.v_sb = ca.k_sb; ca.v_sh = 64; ca.v_ld = 2 * D;
+    ca.o = a.oc; ca.o_sb = (long)S * D; ca.o_sh = 64; ca.o_ld = D;
+    ca.lse = a.lse_c;
+    if (attn_forward(c, ca, err)) return 1;
+    if (lin_fwd(m, wco, nullptr, nullptr, a.oc, M, m.dtmp, nullptr, nullptr, err)) return 1;
+    if (k_add(c, a.x1, m.dtmp, (long)M * D, a.x2, err)) return 1;
+    // feed-forward branch
+    if (k_rmsnorm_mod_fwd(c, a.x2, (int)M, D, g_ff, a.mod + 3 * D, a.mod + 4 * D, ms, S, k.norm_eps, a.hf, a.rstd_f, err))
+      return 1;
+    if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, a.ff, nullptr, a.ut[2], err)) return 1;
+    if (k_swiglu_fwd(c, a.ff, (int)M, I, a.act, err)) return 1;
+    if (lin_fwd(m, wfo, tf, b_fo, a.act, M, a.yf, nullptr, a.ut[3], err)) return 1;
+    if (k_gate_residual(c, a.x2, a.yf, a.mod + 5 * D, ms, (int)M, D, S, x_next, err)) return 1;
+  }
+
+  // ---------------- tail + loss (src/dit.h:314-323, src/train_ckpt.h:223-228)
+  const Weight* wpo = m.weight("dit.proj_out.weight", err);
+  const Weight* wpc = m.weight("dit.post_conv.weight", err);
+  if (!wpo || !wpc) return 1;
+  if (k_copy_rows(c, m.x_final, S, k.mem_tokens, nullptr, m.xT_b, T, 0, B, T, D, err)) return 1;
+  if (lin_fwd(m, wpo, nullptr, nullptr, m.xT_b, MT, m.pout, m.pout_b, nullptr, err)) return 1;
+  if (lin_fwd(m, wpc, nullptr, nullptr, m.pout_b, MT, m.vel, nullptr, nullptr, err)) return 1;
+  if (k_add(c, m.vel, m.pout, (long)MT * k.io, m.vel, err)) return 1;
+  if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, err)) return 1;
+
+  // ---------------- backward
+  if (cudaMemcpyAsync(m.dp, m.dvel, sizeof(float) * MT * k.io, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+    return check_launch("copy", err);
+  if (lin_bwd(m, wpc, nullptr, nullptr, m.pout_b, nullptr, m.dvel, MT, nullptr, m.dp, 1, nullptr, err)) return 1;
+  if (lin_bwd(m, wpo, nullptr, nullptr, m.xT_b, nullptr, m.dp, MT, nullptr, m.dxT, 0, nullptr, err)) return 1;
+  if (cudaMemsetAsync(m.gx, 0, sizeof(float) * M * D, c->stream) != cudaSuccess) return check_launch("memset", err);
+  if (k_copy_rows(c, m.dxT, T, 0, m.gx, nullptr, S, k.mem_tokens, B, T, D, err)) return 1;
+
+  for (int l = k.depth - 1; l >= 0; --l) {
+    DitBlockAct& a = m.blk[l];
+    const Weight *wqkv = m.weight(m.bname(l, "self.qkv.weight"), err), *wout = m.weight(m.bname(l, "self.out.weight"), err);
+    const Weight *wcq = m.weight(m.bname(l, "cross.q.weight"), err), *wco = m.weight(m.bname(l, "cross.out.weight"), err);
+    const Weight *wfp = m.weight(m.bname(l, "ff.proj.weight"), err), *wfo = m.weight(m.bname(l, "ff.out.weight"), err);
+    const float *g_pre = m.vec(m.bname(l, "pre_norm.gamma"), err), *g_q = m.vec(m.bname(l, "self.q_norm.gamma"), err);
+    const float *g_k = m.vec(m.bname(l, "self.k_norm.gamma"), err), *g_cn = m.vec(m.bname(l, "cross_norm.gamma"), err);
+    const float *g_cq = m.vec(m.bname(l, "cross.q_norm.gamma"), err), *g_ff = m.vec(m.bname(l, "ff_norm.gamma"), err);
+    const float *b_fp = m.vec(m.bname(l, "ff.proj.bias"), err), *b_fo = m.vec(m.bname(l, "ff.out.bias"), err);
+    DitTarget *tq = target(m, m.bname(l, "self.qkv.weight")), *to = target(m, m.bname(l, "self.out.weight"));
+    DitTarget *tp = target(m, m.bname(l, "ff.proj.weight")), *tf = target(m, m.bname(l, "ff.out.weight"));
+    const long ms = 6L * D;
+    // feed-forward branch
+    if (k_gate_bwd(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, m.dtmp, err)) return 1;
+    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, m.dtmp, M, a.ut[3], m.dact, 0, nullptr, err)) return 1;
+    if (k_swiglu_bwd(c, m.dact, a.ff, (int)M, I, m.dtmp, err)) return 1;
+    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, m.dtmp, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
+    if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, err)) return 1;
+    // cross-attention branch (context and its projections are frozen: only dq flows)
+    if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, m.gx, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
+    {
+      AttnArgs ca;
+      ca.B = B; ca.H = H; ca.Sq = S; ca.Sk = C; ca.scale = scale; ca.window = -1;
+      ca.q = a.cq; ca.q_sb = (long)S * D; ca.q_sh = 64; ca.q_ld = D;
+      ca.k = a.kvb; ca.k_sb = (long)C * 2 * D; ca.k_sh = 64; ca.k_ld = 2 * D;
+      ca.v = a.kvb + D; ca.v_sb = ca.k_sb; ca.v_sh = 64; ca.v_ld = 2 * D;
+      ca.o = a.oc; ca.o_sb = (long)S * D; ca.o_sh = 64; ca.o_ld = D;
+      ca.lse = a.lse_c;
+      ca.dO = m.dO_b; ca.dO_sb = (long)S * D; ca.dO_sh = 64; ca.dO_ld = D;
+      ca.Dsum = m.Dsum;
+      ca.dq = m.dtmp; ca.dq_sb = (long)S * D; ca.dq_sh = 64; ca.dq_ld = D;
+      if (attn_backward(c, ca, false, err)) return 1;
+      HeadSlice hs;
+      hs.col = 0; hs.gamma = g_cq; hs.rstd = a.rcq;
+      if (k_head_prep_bwd(c, m.dtmp, D, a.qf, (int)M, D, H, hs, S, k.rot, k.rope_base, m.dh, err)) return 1;
+    }
+    if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, m.dh, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
+    if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, err)) return 1;
+    // self-attention branch
+    if (k_gate_bwd(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, m.dtmp, err)) return 1;
+    if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, m.dtmp, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
+    {
+      AttnArgs sa;
+      sa.B = B; sa.H = H; sa.Sq = S; sa.Sk = S; sa.scale = scale; sa.window = -1;
+      sa.q = a.qkvb; sa.q_sb = (long)S * Q; sa.q_sh = 64; sa.q_ld = Q;
+      sa.k = a.qkvb + D; sa.k_sb = sa.q_sb; sa.k_sh = 64; sa.k_ld = Q;
+      sa.v = a.qkvb + 2 * D; sa.v_sb = sa.q_sb; sa.v_sh = 64; sa.v_ld = Q;
+      sa.o = a.oa; sa.o_sb = (long)S * D; sa.o_sh = 64; sa.o_ld = D;
+      sa.lse = a.lse_a;
+      sa.dO = m.dO_b; sa.dO_sb = (long)S * D; sa.dO_sh = 64; sa.dO_ld = D;
+      sa.Dsum = m.Dsum;
+      sa.dq = m.dq3; sa.dq_sb = (long)S * Q; sa.dq_sh = 64; sa.dq_ld = Q;
+      sa.dk = m.dq3 + D; sa.dk_sb = sa.dq_sb; sa.dk_sh = 64; sa.dk_ld = Q;
+      sa.dv = m.dq3 + 2 * D; sa.dv_sb = sa.dq_sb; sa.dv_sh = 64; sa.dv_ld = Q;
+      if (attn_backward(c, sa, true, err)) return 1;
+      HeadSlice hq, hk;
+      hq.col = 0; hq.gamma = g_q; hq.rope = 1; hq.rstd = a.rq;
+      hk.col = D; hk.gamma = g_k; hk.rope = 1; hk.rstd = a.rk;
+      if (k_head_prep_bwd(c, m.dq3, Q, a.qkv, (int)M, Q, H, hq, S, k.rot, k.rope_base, m.dq3, err)) return 1;
+      if (k_head_prep_bwd(c, m.dq3 + D, Q, a.qkv, (int)M, Q, H, hk, S, k.rot, k.rope_base, m.dq3, err)) return 1;
+    }
+    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, m.dq3, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
+    if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, err)) return 1;
+  }
+  return 0;
+}
+
+}  // namespace sa3k
+
+using namespace sa3k;
+
+struct sa3k_dit {
+  DitModel m;
+};
+
+static int dfail(char* err, int len, const std::string& msg) {
+  if (err && len > 0) {
+    std::strncpy(err, msg.c_str(), (size_t)len - 1);
+    err[len - 1] = 0;
+  }
+  return 1;
+}
+
+extern "C" {
+
+int sa3k_dit_create(sa3k_ctx* ctx, const sa3k_dit_config* cfg, sa3k_dit** out, char* err, int err_len) {
+  if (!ctx || !cfg || !out) return dfail(err, err_len, "NULL argument");
+  if (cfg->head_dim != 64) return dfail(err, err_len, "head_dim must be 64");
+  if (cfg->dim != cfg->heads * cfg->head_dim) return dfail(err, err_len, "dim must equal heads * head_dim");
+  if (cfg->dim % 64 || cfg->ff_inner % 64 || cfg->io % 64 || cfg->cond_dim % 64 || cfg->time_dim % 64)
+    return dfail(err, err_len, "dim, ff_inner, io, cond_dim and time_dim must be multiples of 64");
+  if (cfg->rot != 32 && cfg->rot != 64) return dfail(err, err_len, "rot must be 32 or 64");
+  sa3k_dit* d = new (std::nothrow) sa3k_dit();
+  if (!d) return dfail(err, err_len, "out of host memory");
+  d->m.c = &ctx->c;
+  d->m.handle = ctx;
+  d->m.cfg = *cfg;
+  *out = d;
+  return 0;
+}
+
+void sa3k_dit_free(sa3k_dit* d) {
+  if (!d) return;
+  cudaSetDevice(d->m.c->device);
+  cudaStreamSynchronize(d->m.c->stream);
+  delete d;
+}
+
+int sa3k_dit_set_tensor(sa3k_dit* d, const char* name, int type, const void* host, int64_t ne0, int64_t ne1,
+                        char* err, int err_len) {
+  if (!d || !name || !host) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  cudaSetDevice(m.c->device);
+  const std::string n(name);
+  const bool is_weight = n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0;
+  std::string e;
+  if (is_weight) {
+    if (m.W.count(n)) return dfail(err, err_len, "tensor set twice: " + n);
+    // the public upload path repacks the GGUF blocks; the model owns the handle afterwards
+    sa3k_weight* h = nullptr;
+    if (sa3k_weight_upload(m.handle, type, host, ne0, ne1, &h, err, err_len)) return 1;
+    m.weights.push_back(h);
+    m.W[n] = &h->w;
+    return 0;
+  }
+  if (type != SA3K_TYPE_F32) return dfail(err, err_len, "1-D / non-weight tensors must be F32: " + n);
+  const size_t bytes = (size_t)ne0 * (size_t)(ne1 > 0 ? ne1 : 1) * 4;
+  float* dv = static_cast<float*>(dmalloc(m, bytes, e));
+  if (!dv) return dfail(err, err_len, e);
+  if (cudaMemcpy(dv, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return dfail(err, err_len, "copy failed");
+  m.V[n] = dv;
+  return 0;
+}
+
+int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, float alpha, const char* const* names,
+                           int n, char* err, int err_len) {
+  if (!d || !adapter_type || !names || n <= 0) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  cudaSetDevice(m.c->device);
+  const std::string at(adapter_type);
+  if (at != "lora" && at != "dora-rows") return dfail(err, err_len, "adapter type must be lora or dora-rows");
+  if (rank < 1 || rank > 16) return dfail(err, err_len, "rank must be 1..16");
+  if (!m.tg.empty()) return dfail(err, err_len, "adapters already initialised");
+  m.dora = at == "dora-rows";
+  m.rank = rank;
+  m.alpha = alpha;
+  m.s = alpha / (float)rank;
+  int64_t off = 0;
+  std::string e;
+  for (int i = 0; i < n; ++i) {
+    DitTarget t;
+    t.name = names[i];
+    auto it = m.W.find(t.name);
+    if (it == m.W.end()) return dfail(err, err_len, "adapter target has no weight: " + t.name);
+    t.w = it->second;
+    t.in = t.w->in;
+    t.out = t.w->out;
+    t.offA = off; off += (int64_t)rank * t.in;
+    t.offB = off; off += t.out * rank;
+    if (m.dora) { t.offM = off; off += t.out; }
+    m.tix[t.name] = (int)m.tg.size();
+    m.tg.push_back(t);
+  }
+  m.np = off;
+  for (float** b : {&m.p, &m.g, &m.am, &m.av}) {
+    *b = static_cast<float*>(dmalloc(m, (size_t)off * 4, e));
+    if (!*b) return dfail(err, err_len, e);
+    cudaMemsetAsync(*b, 0, (size_t)off * 4, m.c->stream);
+  }
+  size_t prep_bytes = 0;
+  for (DitTarget& t : m.tg) prep_bytes += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
+  char* pm = static_cast<char*>(dmalloc(m, prep_bytes, e));
+  if (!pm) return dfail(err, err_len, e);
+  for (DitTarget& t : m.tg) {
+    AdapterPrep& p = t.prep;
+    p.rank = rank; p.in = t.in; p.out = t.out; p.s = m.s;
+    p.A = m.p + t.offA; p.B = m.p + t.offB;
+    if (m.dora) {
+      t.bns = static_cast<float*>(dmalloc(m, (size_t)t.out * 4, e));
+      if (!t.bns) return dfail(err, err_len, e);
+      p.m = m.p + t.offM;
+      p.bns = t.bns;
+      // base_norm_sq and the magnitude init = row norms of the dequantized base
+      // (train_row_norm_sq / train_row_norms, src/train_lora.h:141-174,262-263)
+      if (weight_row_norms(m.c, t.w, 1e-12f, t.bns, m.p + t.offM, e)) return dfail(err, err_len, e);
+    }
+    adapter_bind(p, pm);
+    pm += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
+  }
+  if (cudaStreamSynchronize(m.c->stream) != cudaSuccess) return dfail(err, err_len, "adapter init failed");
+  return 0;
+}
+
+int64_t sa3k_dit_adapter_size(const sa3k_dit* d) { return d ? d->m.np : 0; }
+
+int sa3k_dit_adapter_offsets(const sa3k_dit* d, int idx, int64_t* offA, int64_t* offB, int64_t* offM) {
+  if (!d || idx < 0 || idx >= (int)d->m.tg.size()) return 1;
+  const DitTarget& t = d->m.tg[(size_t)idx];
+  if (offA) *offA = t.offA;
+  if (offB) *offB = t.offB;
+  if (offM) *offM = t.offM;
+  return 0;
+}
+
+int sa3k_dit_adapter_buffer(sa3k_dit* d, int which, float** dev_ptr, char* err, int err_len) {
+  if (!d || !dev_ptr) return dfail(err, err_len, "NULL argument");
+  float* b[4] = {d->m.p, d->m.g, d->m.am, d->m.av};
+  if (which < 0 || which > 3) return dfail(err, err_len, "which must be 0 (params), 1 (grads), 2 (m), 3 (v)");
+  *dev_ptr = b[which];
+  return 0;
+}
+
+int sa3k_dit_adapter_copy(sa3k_dit* d, int which, float* buf, int64_t offset, int64_t count, int to_model,
+                          char* err, int err_len) {
+  if (!d || !buf) return dfail(err, err_len, "NULL argument");
+  float* b[4] = {d->m.p, d->m.g, d->m.am, d->m.av};
+  if (which < 0 || which > 3) return dfail(err, err_len, "which must be 0..3");
+  if (offset < 0 || count < 0 || offset + count > d->m.np) return dfail(err, err_len, "range outside the state");
+  cudaSetDevice(d->m.c->device);
+  float* dev = b[which] + offset;
+  const cudaError_t e = to_model ? cudaMemcpyAsync(dev, buf, (size_t)count * 4, cudaMemcpyDefault, d->m.c->stream)
+                                 : cudaMemcpyAsync(buf, dev, (size_t)count * 4, cudaMemcpyDefault, d->m.c->stream);
+  if (e != cudaSuccess || cudaStreamSynchronize(d->m.c->stream) != cudaSuccess) return dfail(err, err_len, "copy failed");
+  return 0;
+}
+
+int sa3k_dit_zero_grads(sa3k_dit* d, char* err, int err_len) {
+  if (!d) return dfail(err, err_len, "NULL argument");
+  cudaSetDevice(d->m.c->device);
+  if (cudaMemsetAsync(d->m.g, 0, (size_t)d->m.np * 4, d->m.c->stream) != cudaSuccess)
+    return dfail(err, err_len, "memset failed");
+  return 0;
+}
+
+int sa3k_dit_forward_backward(sa3k_dit* d, int B, int T, int ctx_len, const float* x_t, const float* target,
+                              const float* t_feat, const float* cross, const float* global, float* loss,
+                              char* err, int err_len) {
+  if (!d || !x_t || !target || !t_feat || !cross || !global) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters: call sa3k_dit_init_adapters first");
+  if (B <= 0 || B > 64 || T <= 0 || ctx_len <= 0) return dfail(err, err_len, "bad batch shape");
+  cudaSetDevice(m.c->device);
+  std::string e;
+  if (alloc_acts(m, B, T, ctx_len, e)) return dfail(err, err_len, e);
+  const sa3k_dit_config& k = m.cfg;
+  const cudaStream_t st = m.c->stream;
+  const int64_t MT = (int64_t)B * T;
+  bool ok = cudaMemcpyAsync(m.in_x, x_t, sizeof(float) * MT * k.io, cudaMemcpyDefault, st) == cudaSuccess &&
+            cudaMemcpyAsync(m.in_target, target, sizeof(float) * MT * k.io, cudaMemcpyDefault, st) == cudaSuccess &&
+            cudaMemcpyAsync(m.in_tfeat, t_feat, sizeof(float) * B * k.time_dim, cudaMemcpyDefault, st) == cudaSuccess &&
+            cudaMemcpyAsync(m.in_cross, cross, sizeof(float) * (size_t)B * ctx_len * k.cond_dim, cudaMemcpyDefault,
+                            st) == cudaSuccess &&
+            cudaMemcpyAsync(m.in_glob, global, sizeof(float) * B * k.cond_dim, cudaMemcpyDefault, st) == cudaSuccess;
+  if (!ok) return dfail(err, err_len, "input copy failed");
+  if (dit_step(m, e)) return dfail(err, err_len, e);
+  if (loss && cudaMemcpyAsync(loss, m.loss, sizeof(float) * B, cudaMemcpyDefault, st) != cudaSuccess)
+    return dfail(err, err_len, "loss copy failed");
+  return 0;
+}
+
+int sa3k_dit_apply_adamw(sa3k_dit* d, int count, const sa3k_adamw_params* hp, int step, double* grad_norm_out,
+                         char* err, int err_len) {
+  if (!d) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  return sa3k_average_clip_adamw(m.handle, m.p, m.g, m.am, m.av, m.np, count, hp, step, grad_norm_out, err, err_len);
+}
+
+}  // extern "C"

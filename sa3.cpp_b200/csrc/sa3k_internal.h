@@ -139,3 +139,11 @@ struct GemmDesc {
 int gemm(Ctx* c, const GemmDesc& d, std::string& err);
 
 }  // namespace sa3k
+
+// The opaque handles of the C ABI (include/sa3k.h) wrap the internal objects.
+struct sa3k_ctx {
+  sa3k::Ctx c;
+};
+struct sa3k_weight {
+  sa3k::Weight w;
+};

@@ -21,6 +21,9 @@ ABI_SYMBOLS = (
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
     "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
+    "sa3k_dit_create", "sa3k_dit_free", "sa3k_dit_set_tensor", "sa3k_dit_init_adapters", "sa3k_dit_adapter_size",
+    "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
+    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N = 1, 2, 3
 
@@ -45,6 +48,15 @@ class HeadSliceC(ctypes.Structure):
 
 def t4(t, batch_stride, head_stride, row_stride):
     return Tensor4(ctypes.c_void_p(t.data_ptr()), batch_stride, head_stride, row_stride)
+
+
+DIT_INT_FIELDS = ("io", "dim", "depth", "heads", "head_dim", "cond_dim", "mem_tokens", "rot", "time_dim",
+                  "ff_inner", "differential")
+DIT_FLOAT_FIELDS = ("rope_base", "norm_eps", "qk_eps", "time_min_freq", "time_max_freq")
+
+
+class DitConfigC(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in DIT_INT_FIELDS] + [(n, ctypes.c_float) for n in DIT_FLOAT_FIELDS]
 
 
 class ProfileEntry(ctypes.Structure):
@@ -86,6 +98,18 @@ def lib():
                                               ctypes.POINTER(ctypes.c_double), E, I]
         L.sa3k_profile_enable.argtypes = [P, I, E, I]
         L.sa3k_ctx_set_option.argtypes = [P, I, I64, E, I]
+        L.sa3k_dit_create.argtypes = [P, ctypes.POINTER(DitConfigC), ctypes.POINTER(P), E, I]
+        L.sa3k_dit_free.argtypes = [P]
+        L.sa3k_dit_free.restype = None
+        L.sa3k_dit_set_tensor.argtypes = [P, ctypes.c_char_p, I, P, I64, I64, E, I]
+        L.sa3k_dit_init_adapters.argtypes = [P, ctypes.c_char_p, I, F, ctypes.POINTER(ctypes.c_char_p), I, E, I]
+        L.sa3k_dit_adapter_size.argtypes = [P]
+        L.sa3k_dit_adapter_offsets.argtypes = [P, I, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)]
+        L.sa3k_dit_adapter_buffer.argtypes = [P, I, ctypes.POINTER(P), E, I]
+        L.sa3k_dit_adapter_copy.argtypes = [P, I, P, I64, I64, I, E, I]
+        L.sa3k_dit_zero_grads.argtypes = [P, E, I]
+        L.sa3k_dit_forward_backward.argtypes = [P, I, I, I, P, P, P, P, P, P, E, I]
+        L.sa3k_dit_apply_adamw.argtypes = [P, I, ctypes.POINTER(AdamWParams), I, ctypes.POINTER(ctypes.c_double), E, I]
         T4 = ctypes.POINTER(Tensor4)
         L.sa3k_attention_fwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, P, E, I]
         L.sa3k_attention_bwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, T4, P, T4, T4, T4, E, I]
@@ -93,8 +117,9 @@ def lib():
         L.sa3k_head_prep_bwd.argtypes = [P, P, I64, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, P, E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
-            if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free"):
+            if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free", "sa3k_dit_free"):
                 getattr(L, name).restype = I
+        L.sa3k_dit_adapter_size.restype = I64
         _lib = L
     return _lib
 
@@ -263,3 +288,74 @@ class Weight:
             self.free()
         except Exception:
             pass
+
+
+class Dit:
+    """A DiT training model on a context (sa3k_dit_*): tensors by GGUF name, flat adapter state."""
+
+    def __init__(self, ctx, cfg):
+        self.ctx = ctx
+        c = DitConfigC(**{k: cfg[k] for k in DIT_INT_FIELDS + DIT_FLOAT_FIELDS})
+        self._h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_create(ctx._h, ctypes.byref(c), ctypes.byref(self._h), err, 512), err)
+
+    def close(self):
+        if self._h:
+            lib().sa3k_dit_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_tensor(self, name, qtype, host, ne0, ne1=1):
+        import numpy as np
+        a = np.ascontiguousarray(host)
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_set_tensor(self._h, name.encode(), TYPE_IDS[qtype], a.ctypes.data_as(ctypes.c_void_p),
+                                         ne0, ne1, err, 512), err)
+
+    def init_adapters(self, adapter_type, rank, alpha, names):
+        arr = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_init_adapters(self._h, adapter_type.encode(), rank, alpha, arr, len(names), err, 512), err)
+
+    def size(self):
+        return int(lib().sa3k_dit_adapter_size(self._h))
+
+    def offsets(self, idx):
+        a, b, m = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+        if lib().sa3k_dit_adapter_offsets(self._h, idx, ctypes.byref(a), ctypes.byref(b), ctypes.byref(m)):
+            raise Sa3kError("bad target index")
+        return a.value, b.value, m.value
+
+    def copy(self, which, buf, offset=0, count=None, to_model=True):
+        """which: 0 params, 1 grads, 2 AdamW m, 3 AdamW v; buf: numpy float32 (host) or torch tensor."""
+        n = count if count is not None else (buf.size if hasattr(buf, "size") and not callable(buf.size) else buf.numel())
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_adapter_copy(self._h, which, _ptr(buf), offset, n, 1 if to_model else 0, err, 512), err)
+
+    def buffer_ptr(self, which):
+        p = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(256)
+        _check(lib().sa3k_dit_adapter_buffer(self._h, which, ctypes.byref(p), err, 256), err)
+        return p.value
+
+    def zero_grads(self):
+        err = ctypes.create_string_buffer(256)
+        _check(lib().sa3k_dit_zero_grads(self._h, err, 256), err)
+
+    def forward_backward(self, B, T, ctx_len, x_t, target, t_feat, cross, glob, loss=None):
+        err = ctypes.create_string_buffer(1024)
+        _check(lib().sa3k_dit_forward_backward(self._h, B, T, ctx_len, _ptr(x_t), _ptr(target), _ptr(t_feat),
+                                               _ptr(cross), _ptr(glob), _ptr(loss), err, 1024), err)
+
+    def apply_adamw(self, count, hp, step, want_norm=False):
+        err = ctypes.create_string_buffer(512)
+        norm = ctypes.c_double(0.0)
+        _check(lib().sa3k_dit_apply_adamw(self._h, count, ctypes.byref(hp), step,
+                                          ctypes.byref(norm) if want_norm else None, err, 512), err)
+        return norm.value if want_norm else None

@@ -1,0 +1,140 @@
+"""GPU parity of the whole DiT adapter-training step (sa3k_dit_*) against float64 torch autograd
+through the oracle's restatement of dit_head / dit_block / dit_tail and the MSE loss.
+
+A small DiT (dim 256, 2 blocks, 4 heads, 64 memory tokens' worth of layout at reduced size) with
+Q8_0 base weights and DoRA-rows adapters on self.qkv / self.out / ff.proj / ff.out; both samples
+of the batch run in one pass.  Checked: per-sample loss, every adapter gradient (dA, dB, dm) and
+the parameters after one clipped AdamW update."""
+import math
+
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+CFG = dict(io=64, dim=256, depth=2, heads=4, head_dim=64, cond_dim=64, mem_tokens=8, rot=32, time_dim=64,
+           ff_inner=512, differential=0, rope_base=10000.0, norm_eps=1e-5, qk_eps=1e-6, time_min_freq=0.5,
+           time_max_freq=10000.0)
+B, T, CTX, RANK, ALPHA = 2, 56, 16, 4, 8.0
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _build(ctx, seed=0):
+    import sa3k
+    import dit_synth
+    rng = np.random.default_rng(seed)
+    shapes = dit_synth.tensor_shapes(CFG)
+    dit = sa3k.Dit(ctx, CFG)
+    deq = {}
+    for name, shape in shapes.items():
+        if dit_synth.is_weight(name):
+            std = 1.0 / math.sqrt(shape[1])
+            w = dit_synth.synth_tensor(name, shape, rng, std)
+            raw = oracle.quantize(w, "q8_0")
+            dit.set_tensor(name, "q8_0", raw, shape[1], shape[0])
+            deq[name] = oracle.dequantize(raw, "q8_0", shape[0], shape[1])
+        else:
+            v = dit_synth.synth_tensor(name, shape, rng, 0.0)
+            dit.set_tensor(name, "f32", v, shape[-1], shape[0] if len(shape) > 1 else 1)
+            deq[name] = v
+    targets = dit_synth.default_targets(CFG)
+    dit.init_adapters("dora-rows", RANK, ALPHA, targets)
+    # adapter values: A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.05), m = row norm * U(0.9, 1.1)
+    flat = np.zeros(dit.size(), np.float32)
+    dit.copy(0, flat, to_model=False)   # m initialised by the device (row norms)
+    ad = {}
+    for i, name in enumerate(targets):
+        oa, ob, om = dit.offsets(i)
+        out, inn = shapes[name]
+        A = rng.normal(0, 1 / math.sqrt(inn), (RANK, inn)).astype(np.float32)
+        Bm = rng.normal(0, 0.05, (out, RANK)).astype(np.float32)
+        m_dev = flat[om:om + out].copy()
+        m = (m_dev * rng.uniform(0.9, 1.1, out)).astype(np.float32)
+        flat[oa:oa + A.size] = A.ravel()
+        flat[ob:ob + Bm.size] = Bm.ravel()
+        flat[om:om + out] = m
+        ad[name] = dict(A=A, B=Bm, m=m, m_dev=m_dev, offs=(oa, ob, om))
+    dit.copy(0, flat, to_model=True)
+    return dit, deq, ad, targets, rng
+
+
+def _inputs(rng):
+    x_t = rng.standard_normal((B, T, CFG["io"])).astype(np.float32)
+    target = rng.standard_normal((B, T, CFG["io"])).astype(np.float32)
+    ts = [0.3, 0.8]
+    tfeat = np.stack([oracle.expo_features(t, CFG["time_dim"], CFG["time_min_freq"], CFG["time_max_freq"])
+                      for t in ts]).astype(np.float32)
+    cross = rng.standard_normal((B, CTX, CFG["cond_dim"])).astype(np.float32)
+    glob = rng.standard_normal((B, CFG["cond_dim"])).astype(np.float32)
+    return x_t, target, tfeat, cross, glob
+
+
+def _reference(deq, ad, inputs):
+    import torch
+    x_t, target, tfeat, cross, glob = inputs
+    c = oracle.DitCfg(io=CFG["io"], dim=CFG["dim"], depth=CFG["depth"], heads=CFG["heads"], cond_dim=CFG["cond_dim"],
+                      mem_tokens=CFG["mem_tokens"], rot=CFG["rot"], time_dim=CFG["time_dim"], ff_inner=CFG["ff_inner"])
+    T64 = lambda a: torch.tensor(np.asarray(a, np.float64))
+    Wd = {k: T64(v) for k, v in deq.items()}
+    lora, leaves = {}, {}
+    for name, p in ad.items():
+        A, Bm, m = T64(p["A"]).requires_grad_(True), T64(p["B"]).requires_grad_(True), T64(p["m"]).requires_grad_(True)
+        bns, _ = oracle.row_norms(deq[name])
+        lora[name] = dict(A=A, B=Bm, m=m, bns=T64(bns), scale=ALPHA / RANK)
+        leaves[name] = (A, Bm, m)
+    losses = [oracle.dit_loss(Wd, lora, T64(x_t[b]), T64(tfeat[b]), T64(cross[b]), T64(glob[b]), T64(target[b]), c)
+              for b in range(B)]
+    sum(losses).backward()
+    grads = {n: tuple(t.grad.numpy() for t in v) for n, v in leaves.items()}
+    return np.array([float(l) for l in losses]), grads
+
+
+def test_dit_step_matches_oracle(ctx):
+    import torch
+    dit, deq, ad, targets, rng = _build(ctx)
+    # the device initialises m to the dequantized base row norms (train_row_norms)
+    for name in targets:
+        _, nrm = oracle.row_norms(deq[name])
+        np.testing.assert_allclose(ad[name]["m_dev"], nrm, rtol=1e-6)
+    inputs = _inputs(rng)
+    ref_loss, ref_grads = _reference(deq, ad, inputs)
+
+    dit.zero_grads()
+    loss = np.zeros(B, np.float32)
+    dit.forward_backward(B, T, CTX, *inputs, loss=loss)
+    ctx.sync()
+    assert np.max(np.abs(loss - ref_loss) / ref_loss) < 1e-2, (loss, ref_loss)
+    grads = np.zeros(dit.size(), np.float32)
+    dit.copy(1, grads, to_model=False)
+    worst = {}
+    for name in targets:
+        oa, ob, om = ad[name]["offs"]
+        gA, gB, gm = ref_grads[name]
+        got = (grads[oa:oa + gA.size].reshape(gA.shape), grads[ob:ob + gB.size].reshape(gB.shape),
+               grads[om:om + gm.size])
+        for lab, g, r in zip(("dA", "dB", "dm"), got, (gA, gB, gm)):
+            worst[f"{name}:{lab}"] = rel_l2(g, r)
+    bad = {k: v for k, v in worst.items() if not v < 2e-2}
+    assert not bad, bad
+
+    # one averaged (count = B) + clipped AdamW update on the flat state
+    import sa3k
+    p0 = np.zeros(dit.size(), np.float32)
+    dit.copy(0, p0, to_model=False)
+    hp = sa3k.AdamWParams(1e-3, 0.9, 0.999, 1e-8, 0.01, 1.0)
+    norm = dit.apply_adamw(B, hp, 1, want_norm=True)
+    p1 = np.zeros(dit.size(), np.float32)
+    dit.copy(0, p1, to_model=False)
+    g = grads.copy()
+    ref_norm = oracle.average_and_clip([g], B, 1.0)
+    rp = p0.copy()
+    oracle.adamw_f32(rp, g, np.zeros_like(rp), np.zeros_like(rp), 1e-3, 0.9, 0.999, 1e-8, 0.01, 1)
+    assert abs(norm - ref_norm) <= 1e-6 * ref_norm
+    np.testing.assert_allclose(p1, rp, rtol=1e-6, atol=1e-8)
