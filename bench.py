@@ -1,24 +1,20 @@
 """Benchmark of the sa3.cpp adapter-training hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sa3k|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl sa3k|reference] [--workload dit|linear]
 
-One step = one training step of the BASELINE workload on every rank: forward + backward of the
-frozen-base adapted linear over one sample, the NCCL gradient all-reduce across ranks
-(data parallel, one sample per rank), then the averaged + clipped AdamW update of the adapter
-(the reference's train_apply_accumulated_adamw, src/train_loop.h:173-211).
+Headline workload (BASELINE.json configs[3] / [4]): one training step of the medium-like DiT
+(d 1536, 24 blocks, Q8_0 frozen base, DoRA r16 on qkv / out / ff.proj / ff.out) on batch 4 per
+GPU: forward + backward through the sa3k DiT step, the NCCL all-reduce of the adapter gradients
+across ranks (data parallel), then the averaged + clipped AdamW update.  Seeded synthetic
+weights and inputs.  Unit: samples/s summed over all ranks.
 
-Workload: DoRA rank 16 / alpha 16 on the MLP up-projection
-1536 -> 6144 with a Q4_K base (N(0, 0.02)), 2048 tokens per sample, X and dY ~ N(0, 1), seeded
-synthetic data (no dataset is involved).  The unit is samples/s summed over all ranks.
+Reported beside the device-timed value: the GEMM engine's roofline (algorithmic FLOPs / its summed
+CUDA-event time inside a replayed graph, against the measured bf16 peak), the same GEMMs through
+the in-smem Q8_0 dequant path, the e2e value through the C ABI with pinned host inputs, a CPU
+restatement baseline, nvidia-smi clocks sampled during the timed region and the launch count.
 
-Reported beside the device-timed value:
-  roofline      the two quant-GEMM kernels (forward Y and backward dX), algorithmic FLOPs / their
-                summed CUDA-event time in a timed pass, against the measured bf16 peak
-  e2e           the same step through the C ABI with the inputs copied from pinned host memory and
-                the output read back every step
-  cpu_baseline  the CPU restatement (oracle, float32 numpy/BLAS on all host threads)
-  clocks        nvidia-smi samples taken during the timed region
-Rank 0 prints one JSON line.
+--workload linear: BASELINE configs[1] (one DoRA Q4_K 1536 -> 6144 linear, 2048 tokens) as a
+component benchmark.  Rank 0 prints one JSON line.
 """
 import argparse
 import json
@@ -47,7 +43,7 @@ def load_peaks():
     return 1590.0, 6650.0, "fallback"
 
 
-def synth(seed):
+def linear_synth(seed):
     """Seeded synthetic weights and sample for one rank (float32 numpy)."""
     rng = np.random.default_rng(seed)
     W = rng.normal(0, 0.02, (OUT, IN)).astype(np.float32)
@@ -112,7 +108,7 @@ def _oracle():
     return oracle
 
 
-def cpu_reference_step(W, A, B, bias, x, dy, m, bns, p, mom, vel, step):
+def linear_cpu_step(W, A, B, bias, x, dy, m, bns, p, mom, vel, step):
     """One step of the CPU restatement: float32 forward + backward + AdamW (oracle)."""
     oracle = _oracle()
     y, cache = oracle.dit_lin_fwd(x, W, A, B, ALPHA / RANK, m, bns, bias, dtype=np.float32)
@@ -123,10 +119,10 @@ def cpu_reference_step(W, A, B, bias, x, dy, m, bns, p, mom, vel, step):
     return y
 
 
-def cpu_baseline(seed, budget_s=15.0, max_reps=5):
+def linear_cpu_baseline(seed, budget_s=15.0, max_reps=5):
     """Time the CPU restatement on the full sample, repeated within a bounded budget."""
     oracle = _oracle()
-    W, A, B, bias, x, dy = synth(seed)
+    W, A, B, bias, x, dy = linear_synth(seed)
     Wd = oracle.dequantize(oracle.quantize(W, QTYPE), QTYPE, OUT, IN)
     bns, nrm = oracle.row_norms(Wd)
     m = nrm.copy()
@@ -134,12 +130,12 @@ def cpu_baseline(seed, budget_s=15.0, max_reps=5):
     p = np.concatenate([A.ravel(), B.ravel(), m]).astype(np.float32)
     mom = np.zeros(n, np.float32)
     vel = np.zeros(n, np.float32)
-    cpu_reference_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, 1)   # warm-up
+    linear_cpu_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, 1)   # warm-up
     times = []
     t_start = time.perf_counter()
     for rep in range(max_reps):
         t0 = time.perf_counter()
-        cpu_reference_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, rep + 2)
+        linear_cpu_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, rep + 2)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() - t_start > budget_s:
             break
@@ -150,12 +146,12 @@ def cpu_baseline(seed, budget_s=15.0, max_reps=5):
                       f"kernels, is not available)"}
 
 
-def run_reference(args):
+def run_linear_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     oracle = _oracle()
-    W, A, B, bias, x, dy = synth(1000)
+    W, A, B, bias, x, dy = linear_synth(1000)
     Wd = oracle.dequantize(oracle.quantize(W, QTYPE), QTYPE, OUT, IN)
     bns, nrm = oracle.row_norms(Wd)
     m = nrm.copy()
@@ -164,10 +160,10 @@ def run_reference(args):
     mom = np.zeros(n, np.float32)
     vel = np.zeros(n, np.float32)
     for i in range(args.warmup):
-        cpu_reference_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, i + 1)
+        linear_cpu_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, i + 1)
     t0 = time.perf_counter()
     for i in range(args.steps):
-        cpu_reference_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, args.warmup + i + 1)
+        linear_cpu_step(Wd, A, B, bias, x, dy, m, bns, p, mom, vel, args.warmup + i + 1)
     dt = time.perf_counter() - t0
     value = args.steps / dt
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
@@ -183,17 +179,8 @@ def run_reference(args):
     return 0
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
-    if args.impl == "reference":
-        return run_reference(args)
+def main_linear(args):
+    """BASELINE config 2 (one DoRA Q4_K linear) as a component benchmark: --workload linear."""
 
     import torch
     import torch.distributed as dist
@@ -210,7 +197,7 @@ def main():
     dev = torch.device("cuda", local)
 
     ctx = sa3k.Context(local)
-    W, A, B, bias, x_h, dy_h = synth(1000 + rank)
+    W, A, B, bias, x_h, dy_h = linear_synth(1000 + rank)
     w = ctx.upload(gguf_blocks.encode(W, QTYPE), QTYPE, IN, OUT)
     bns = torch.empty(OUT, device=dev)
     nrm = torch.empty(OUT, device=dev)
@@ -352,7 +339,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(2000)
+        cpu = linear_cpu_baseline(2000)
 
     if rank == 0:
         line = {
@@ -377,6 +364,7 @@ def main():
             "e2e": {"value": e2e_val, "unit": "samples/s",
                     "h2d_bytes_per_step": x_h.nbytes + dy_h.nbytes, "d2h_bytes_per_step": S * OUT * 4},
             "gpu_launches": launches,
+            "graph_kernel_nodes": nodes,
             "clocks": clk.summary(),
             "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())},
             "graph": "fwd+bwd (+all-reduce) replayed from a CUDA graph; AdamW launched eagerly per step",
@@ -386,6 +374,381 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# =============================================================================== DiT workload
+
+DIT_B, DIT_T, DIT_CTX, DIT_RANK, DIT_ALPHA = 4, 1024, 128, 16, 16.0
+DIT_WORKLOAD = ("config4: medium-like DiT (d 1536, 24 blocks, 24 heads, FF 4x SwiGLU, io 64, 64 memory "
+                "tokens, 1024 frames, cross-attention to 128x768), Q8_0 frozen base N(0,0.02), DoRA r16/a16 on "
+                "self.qkv / self.out / ff.proj / ff.out, batch 4 per GPU; fwd + bwd + NCCL grad all-reduce + "
+                "averaged, clipped AdamW (lr 1e-4, betas 0.9/0.999, wd 0.01, clip 1.0)")
+
+
+def dit_cfg():
+    sys.path.insert(0, os.path.join(REPO, "sa3.cpp_b200"))
+    import dit_synth
+    return dict(dit_synth.MEDIUM_LIKE)
+
+
+def dit_linear_flops(cfg, B, T, C):
+    """Algorithmic FLOPs of the frozen-base GEMMs (classes linear.fwd + linear.dx) of one step."""
+    D, I, io, cd, td = cfg["dim"], cfg["ff_inner"], cfg["io"], cfg["cond_dim"], cfg["time_dim"]
+    S = cfg["mem_tokens"] + T
+    M, MT, MC = B * S, B * T, B * C
+    fwd = [(B, td, D), (B, D, D), (B, cd, D), (B, D, D), (B, D, D), (B, D, 6 * D), (MC, cd, D), (MC, D, D),
+           (MT, io, io), (MT, io, D), (MT, D, io), (MT, io, io)]
+    dx = [(MT, D, io), (MT, io, io)]
+    for _ in range(cfg["depth"]):
+        blk = [(M, D, 3 * D), (M, D, D), (M, D, D), (M, D, D), (M, D, 2 * I), (M, I, D)]
+        fwd += blk + [(MC, D, 2 * D)]
+        dx += blk
+    return sum(2.0 * r * i * o for r, i, o in fwd + dx)
+
+
+def dit_attention_flops(cfg, B, T, C):
+    """Algorithmic attention FLOPs of one step: 2 matmuls forward, 5 backward (dq pass of the cross
+    attention: 3), per head."""
+    S, H = cfg["mem_tokens"] + T, cfg["heads"]
+    self_f = 2 * 2.0 * S * S * 64 * H * B
+    cross_f = 2 * 2.0 * S * C * 64 * H * B
+    return cfg["depth"] * (self_f * (1 + 2.5) + cross_f * (1 + 1.5))
+
+
+def build_dit(ctx, cfg, seed):
+    """A seeded synthetic checkpoint uploaded as GGUF Q8_0 rows (weights made and encoded on the GPU)."""
+    import torch
+    import sa3k
+    import dit_synth
+    import gguf_blocks
+    dit = sa3k.Dit(ctx, cfg)
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    for name, shape in dit_synth.tensor_shapes(cfg).items():
+        if dit_synth.is_weight(name):
+            w = torch.randn(shape, generator=gen, device="cuda") * 0.02
+            dit.set_tensor(name, "q8_0", gguf_blocks.q8_0_torch(w), shape[1], shape[0])
+            del w
+        else:
+            v = dit_synth.synth_tensor(name, shape, rng, 0.0)
+            dit.set_tensor(name, "f32", v, shape[-1], shape[0] if len(shape) > 1 else 1)
+    targets = dit_synth.default_targets(cfg)
+    dit.init_adapters("dora-rows", DIT_RANK, DIT_ALPHA, targets)
+    # A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.01) so every gradient is non-trivial; m = base row norms
+    shapes = dit_synth.tensor_shapes(cfg)
+    p = torch.empty(dit.size(), device="cuda")
+    dit.copy(0, p, to_model=False)
+    for i, name in enumerate(targets):
+        oa, ob, _ = dit.offsets(i)
+        out, inn = shapes[name]
+        p[oa:oa + DIT_RANK * inn].normal_(0.0, 1.0 / np.sqrt(inn), generator=gen)
+        p[ob:ob + out * DIT_RANK].normal_(0.0, 0.01, generator=gen)
+    dit.copy(0, p, to_model=True)
+    torch.cuda.synchronize()
+    return dit
+
+
+def dit_inputs(cfg, B, seed):
+    """One batch: latents z ~ N(0,1), t ~ U(0,1), noise ~ N(0,1) -> x_t, v target (sample_at),
+    Fourier time features, cross [B][128][768] and global [B][768] conditioning ~ N(0,1)."""
+    import train_inputs
+    rng = np.random.default_rng(seed)
+    z = rng.standard_normal((B, DIT_T, cfg["io"])).astype(np.float32)
+    n = rng.standard_normal((B, DIT_T, cfg["io"])).astype(np.float32)
+    ts = rng.uniform(0, 1, B).astype(np.float32)
+    xt = np.empty_like(z)
+    tg = np.empty_like(z)
+    for b in range(B):
+        xt[b], tg[b] = train_inputs.sample_at(z[b], ts[b], n[b])
+    tf = np.stack([train_inputs.expo_features(t, cfg["time_dim"], cfg["time_min_freq"], cfg["time_max_freq"])
+                   for t in ts]).astype(np.float32)
+    cross = rng.standard_normal((B, DIT_CTX, cfg["cond_dim"])).astype(np.float32)
+    glob = rng.standard_normal((B, cfg["cond_dim"])).astype(np.float32)
+    return [xt, tg, tf, cross, glob]
+
+
+def dit_cpu_block(cfg, seed, reps=1):
+    """Time one block of one sample, forward + backward, of the CPU restatement (torch float32
+    autograd over oracle.dit_block, all host threads); returns seconds per block."""
+    import torch
+    oracle = _oracle()
+    import dit_synth
+    torch.set_num_threads(os.cpu_count())
+    g = torch.Generator().manual_seed(seed)
+    shapes = dit_synth.tensor_shapes(dict(cfg, depth=1))
+    Wd, lora = {}, {}
+    for name, shape in shapes.items():
+        if name.startswith("dit.0."):
+            if dit_synth.is_weight(name):
+                Wd[name] = torch.randn(shape, generator=g) * 0.02
+            else:
+                Wd[name] = torch.ones(shape) if name.endswith("gamma") else torch.randn(shape, generator=g) * 0.05
+    for name in dit_synth.default_targets(dict(cfg, depth=1)):
+        out, inn = shapes[name]
+        W = Wd[name]
+        lora[name] = dict(A=(torch.randn(DIT_RANK, inn, generator=g) / inn ** 0.5).requires_grad_(True),
+                          B=(torch.randn(out, DIT_RANK, generator=g) * 0.01).requires_grad_(True),
+                          m=W.norm(dim=1).clone().requires_grad_(True), bns=(W * W).sum(1), scale=1.0)
+    c = oracle.DitCfg(**{k: cfg[k] for k in ("io", "dim", "heads", "cond_dim", "mem_tokens", "rot", "time_dim",
+                                             "ff_inner")}, depth=1)
+    S = cfg["mem_tokens"] + DIT_T
+    x = torch.randn(S, cfg["dim"], generator=g)
+    ctx = torch.randn(DIT_CTX, cfg["dim"], generator=g)
+    gcond = torch.randn(6 * cfg["dim"], generator=g) * 0.1
+    pos = torch.arange(S)
+    times = []
+    for _ in range(reps + 1):
+        t0 = time.perf_counter()
+        y = oracle.dit_block(Wd, lora, "dit.0.", x, ctx, gcond, pos, c)
+        y.sum().backward()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times[1:]) if reps > 0 else times[0]
+
+
+def dit_cpu_baseline(cfg):
+    sec = dit_cpu_block(cfg, 7, reps=2)
+    per_sample = sec * cfg["depth"]
+    return {"value": 1.0 / per_sample, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"one DiT block of one 1088-token sample, forward + backward, float32 torch CPU restatement "
+                      f"(oracle.dit_block) on {os.cpu_count()} threads, median of 2 = {sec:.2f} s, x {cfg['depth']} "
+                      f"blocks per sample (head / tail < 1% of the FLOPs; ggml, which holds the reference's CPU "
+                      f"kernels, is not available)"}
+
+
+def run_dit_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = dit_cfg()
+    for _ in range(max(1, min(args.warmup, 1))):
+        dit_cpu_block(cfg, 7, reps=0)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        dit_cpu_block(cfg, 8 + i, reps=0)
+    dt = (time.perf_counter() - t0) / args.steps * cfg["depth"]   # seconds per sample
+    value = 1.0 / dt
+    sample = (f"each step: one DiT block of one sample fwd+bwd (float32 torch CPU restatement, "
+              f"{os.cpu_count()} threads) x {cfg['depth']} blocks")
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": DIT_WORKLOAD, "global_batch": 1, "seq_len": DIT_T, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def graph_kernel_nodes(g):
+    """Kernel nodes of a captured graph by owner ({"sa3k": n, "other": n}), read back through the
+    driver API as a cross-check of the library's own launch count; None when unavailable."""
+    try:
+        from cuda.bindings import driver as d
+        cg = d.CUgraph(g.raw_cuda_graph())
+        _, _, n = d.cuGraphGetNodes(cg, 0)
+        _, nodes, n = d.cuGraphGetNodes(cg, n)
+        out = {"sa3k": 0, "other": 0}
+        for nd in nodes[:n]:
+            _, t = d.cuGraphNodeGetType(nd)
+            if t != d.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+                continue
+            _, prm = d.cuGraphKernelNodeGetParams(nd)
+            _, name = d.cuFuncGetName(prm.func)
+            name = name.decode() if isinstance(name, bytes) else str(name)
+            out["other" if "nccl" in name.lower() else "sa3k"] += 1
+        return out
+    except Exception as e:  # noqa: BLE001 - the count is a cross-check only
+        return {"unavailable": str(e)[:120]}
+
+
+class _DevBuf:
+    """A raw device pointer seen by torch through __cuda_array_interface__ (zero copy)."""
+
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (n,), "typestr": "<f4", "version": 2}
+
+
+def main_dit(args):
+    import torch
+    import torch.distributed as dist
+    import sa3k
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    cfg = dit_cfg()
+    B, T, C = DIT_B, DIT_T, DIT_CTX
+    ctx = sa3k.Context(local)
+    dit = build_dit(ctx, cfg, seed=1234)                 # identical base + adapters on every rank
+    grads = torch.as_tensor(_DevBuf(dit.buffer_ptr(1), dit.size()), device=dev)
+    hp = sa3k.AdamWParams(1e-4, 0.9, 0.999, 1e-8, 0.01, 1.0)
+    host_in = dit_inputs(cfg, B, seed=100 + rank)       # each rank its own samples
+    dev_in = [torch.from_numpy(a).to(dev) for a in host_in]
+    loss_dev = torch.zeros(B, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, device=dev)
+    state = {"step": 0}
+
+    def fwd_bwd(inputs, loss):
+        dit.zero_grads()
+        dit.forward_backward(B, T, C, *inputs, loss=loss)
+        if world > 1:
+            dist.all_reduce(grads)
+
+    def adam():
+        state["step"] += 1
+        dit.apply_adamw(B * world, hp, state["step"])
+
+    def capture(timing, inputs, loss):
+        ctx.profile_enable(timing=timing)
+        g = torch.cuda.CUDAGraph(keep_graph=True)
+        with torch.cuda.graph(g):
+            ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+            fwd_bwd(inputs, loss)
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        g.instantiate()
+        return g
+
+    def timed(fn, k):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record()
+            fn()
+            e1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t = torch.tensor([sum(e0.elapsed_time(e1) for e0, e1 in evs)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):                         # eager warm-up: allocates the activation arena
+        fwd_bwd(dev_in, loss_dev)
+        adam()
+    ctx.sync()
+
+    # ---- pass 1: headline, device-resident inputs, the step replayed from a CUDA graph
+    graph = capture(0, dev_in, loss_dev)
+    per_graph = sum(v[0] for v in ctx.profile_read().values())
+    nodes = graph_kernel_nodes(graph)
+
+    def graph_step():
+        graph.replay()
+        adam()
+
+    for _ in range(3):
+        graph_step()
+    ctx.profile_enable(timing=0)
+    with Clocks(local) as clk:
+        total_ms = timed(graph_step, args.steps)
+    launches = per_graph * args.steps + sum(v[0] for v in ctx.profile_read().values())
+    value = world * B * args.steps / (total_ms / 1000.0)
+    loss_now = float(loss_dev.mean().item())
+
+    # ---- pass 2: per-kernel CUDA events captured in the graph -> roofline of the GEMM engine
+    peak_tf, peak_hbm, peak_kind = load_peaks()
+    gflops = dit_linear_flops(cfg, B, T, C)
+
+    def profiled(smem_dequant, k):
+        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 1 if smem_dequant else 0)
+        g = capture(2, dev_in, loss_dev)
+        acc = {}
+        for _ in range(k):
+            flush.zero_()
+            g.replay()
+            for name, (n_l, ms) in ctx.profile_read().items():
+                a = acc.setdefault(name, [0, 0.0])
+                a[0] += n_l
+                a[1] += ms
+        ctx.profile_enable(timing=0)
+        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
+        del g
+        ms_g = acc["linear.fwd"][1] + acc["linear.dx"][1]
+        return acc, ms_g, gflops * k / (ms_g / 1000.0) / 1e12
+
+    kprof = max(2, min(args.steps, 5))
+    prof, ms_gemm, achieved = profiled(False, kprof)
+    prof_q, ms_q, achieved_q = profiled(True, 2)
+
+    # ---- pass 3: e2e, eager calls of the C ABI with pinned host inputs copied in and the loss read back
+    pin_in = [torch.from_numpy(a).pin_memory() for a in host_in]
+    loss_pin = torch.zeros(B, pin_memory=True)
+
+    def e2e_step():
+        fwd_bwd(pin_in, loss_pin)
+        adam()
+
+    e2e_ms = timed(e2e_step, args.steps)
+    e2e_val = world * B * args.steps / (e2e_ms / 1000.0)
+    ctx.sync()
+    del graph
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = dit_cpu_baseline(cfg)
+    step_flops = gflops + dit_attention_flops(cfg, B, T, C)
+    if rank == 0:
+        ms_step = total_ms / args.steps
+        line = {
+            "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": DIT_WORKLOAD, "global_batch": B * world, "seq_len": T,
+                       "parallelism": f"dp{world}", "l2": "256 MB flush between timed steps"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "traffic": None,
+                         "kernel": "tcgen05 GEMM engine, classes linear.fwd + linear.dx (all frozen-base "
+                                   "projections of the step; Q8_0 base via its bf16 operand copy)",
+                         "peak_kind": f"{peak_kind} bf16 burst",
+                         "kernel_ms_per_step": ms_gemm / kprof, "algorithmic_tflop_per_step": gflops / 1e12},
+            "quant_gemm_smem_dequant": {
+                "achieved": achieved_q, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved_q / peak_tf,
+                "kernel": "the same GEMMs with TMA-loaded Q8_0 codes dequantized in shared memory",
+                "kernel_ms_per_step": ms_q / 2},
+            "step_tflops": {"algorithmic_tflop": step_flops / 1e12,
+                            "achieved": step_flops / (ms_step / 1000.0) / 1e12,
+                            "frac_of_peak": step_flops / (ms_step / 1000.0) / 1e12 / peak_tf},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": "samples/s",
+                    "h2d_bytes_per_step": int(sum(a.nbytes for a in host_in)), "d2h_bytes_per_step": B * 4},
+            "gpu_launches": launches,
+            "graph_kernel_nodes": nodes,
+            "clocks": clk.summary(),
+            "loss": loss_now,
+            "graph": "fwd+bwd (+all-reduce) replayed from a CUDA graph; AdamW launched eagerly per step",
+            "kernels": {k: {"launches": v[0], "ms_per_step": round(v[1] / kprof, 4)} for k, v in sorted(prof.items())},
+        }
+        print(json.dumps(line), flush=True)
+    dit.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "linear"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.workload == "linear":
+        return run_linear_reference(args) if args.impl == "reference" else main_linear(args)
+    return run_dit_reference(args) if args.impl == "reference" else main_dit(args)
 
 
 if __name__ == "__main__":

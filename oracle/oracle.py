@@ -253,8 +253,8 @@ def rope_neox(x, pos, n_dims, base):
     half = n_dims // 2
     i = torch.arange(half, dtype=torch.float64)
     theta = pos.to(torch.float64)[:, None] * torch.pow(torch.tensor(base, dtype=torch.float64), -2.0 * i / n_dims)
-    c = torch.cos(theta)[:, None, :]
-    s = torch.sin(theta)[:, None, :]
+    c = torch.cos(theta)[:, None, :].to(x.dtype)
+    s = torch.sin(theta)[:, None, :].to(x.dtype)
     x0, x1, rest = x[..., :half], x[..., half:n_dims], x[..., n_dims:]
     return torch.cat([x0 * c - x1 * s, x0 * s + x1 * c, rest], -1)
 

@@ -73,3 +73,19 @@ def encode(w, qtype):
         w32 = np.ascontiguousarray(w, np.float32)
         return w32.view(np.uint8).reshape(w.shape[0], -1)
     raise ValueError(qtype)
+
+
+def q8_0_torch(w):
+    """Q8_0 row bytes of a CUDA float32 tensor [out][in] (a valid encoding, built on the GPU so that
+    billion-parameter synthetic checkpoints are quick to make); returns a host uint8 array."""
+    import torch
+    out, inn = w.shape
+    assert inn % 32 == 0
+    b = w.reshape(out, inn // 32, 32)
+    d = (b.abs().amax(-1, keepdim=True) / 127.0).to(torch.float32)
+    inv = torch.where(d == 0, torch.zeros_like(d), 1.0 / d)
+    q = torch.round(b * inv).clamp_(-127, 127).to(torch.int8)
+    blk = torch.empty(out, inn // 32, 34, dtype=torch.uint8, device=w.device)
+    blk[..., :2] = d.to(torch.float16).view(torch.uint8)
+    blk[..., 2:] = q.view(torch.uint8)
+    return blk.reshape(out, -1).cpu().numpy()

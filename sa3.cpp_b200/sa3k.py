@@ -175,9 +175,11 @@ class Context:
         except Exception:
             pass
 
-    def profile_enable(self, timing=True):
+    def profile_enable(self, timing=1):
+        """timing 0: count launches only; 1: time each launch class with events (eager);
+        2: events captured into a CUDA graph, re-read after each replay."""
         err = ctypes.create_string_buffer(256)
-        _check(lib().sa3k_profile_enable(self._h, 1 if timing else 0, err, 256), err)
+        _check(lib().sa3k_profile_enable(self._h, int(timing), err, 256), err)
 
     def profile_read(self):
         """{class name: (launches, total_ms)} since the last profile_enable."""

@@ -74,3 +74,18 @@ def test_diffusion_sample_matches_reference():
     xt = (np.float32(1) - t) * z + t * n
     assert np.array_equal(xt, g["x_t"])
     assert np.array_equal(n - z, g["v"])
+
+
+def test_package_sample_at_matches_reference_diffusion():
+    import train_inputs
+    g = np.load(os.path.join(GOLD, "diffusion.npz"))
+    xt, v = train_inputs.sample_at(g["z"], g["t"], g["noise"])
+    assert np.array_equal(xt, g["x_t"]) and np.array_equal(v, g["v"])
+
+
+def test_package_expo_features_matches_restatement():
+    import train_inputs
+    for t in (0.0, 0.3, 0.999):
+        a = train_inputs.expo_features(t, 256, 0.5, 10000.0)
+        b = oracle.expo_features(t, 256, 0.5, 10000.0)
+        np.testing.assert_allclose(a, b, rtol=0, atol=2e-6)
