@@ -364,7 +364,6 @@ def main_linear(args):
             "e2e": {"value": e2e_val, "unit": "samples/s",
                     "h2d_bytes_per_step": x_h.nbytes + dy_h.nbytes, "d2h_bytes_per_step": S * OUT * 4},
             "gpu_launches": launches,
-            "graph_kernel_nodes": nodes,
             "clocks": clk.summary(),
             "kernels": {k: {"launches": v[0], "ms": round(v[1], 4)} for k, v in sorted(prof.items())},
             "graph": "fwd+bwd (+all-reduce) replayed from a CUDA graph; AdamW launched eagerly per step",
