@@ -171,6 +171,24 @@ int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim
                        const float* lse, const sa3k_tensor4* dq, const sa3k_tensor4* dk,
                        const sa3k_tensor4* dv, char* err, int err_len);
 
+/* sa3k_attention_bwd that never allocates device memory.  No counterpart in the reference: it is
+ * for callers that must not allocate during a step -- a process whose device memory is all
+ * pre-reserved by its own pool (a cudaMalloc would fail or fragment it), or a latency-sensitive
+ * caller that cannot afford the device-wide synchronisation cudaMalloc / cudaFree may imply.
+ * Its only scratch (one float per (batch, head, query row)) is a fixed device array inside the
+ * library: B*H*Sq must be <= 1,048,576 (4 MiB), larger sizes are rejected with an error.  The
+ * first call on each device looks up that array's address (cudaGetSymbolAddress, which may load
+ * the library's device code); make that first call before capturing a stream.  All calls on one
+ * device share the array, so two calls in flight at the same time (other streams, other
+ * contexts, other threads) race: serialise them.  Same arguments and results as
+ * sa3k_attention_bwd. */
+int sa3k_attention_bwd_noalloc(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim,
+                               float scale, int window, const sa3k_tensor4* q,
+                               const sa3k_tensor4* k, const sa3k_tensor4* v,
+                               const sa3k_tensor4* o, const sa3k_tensor4* dO, const float* lse,
+                               const sa3k_tensor4* dq, const sa3k_tensor4* dk,
+                               const sa3k_tensor4* dv, char* err, int err_len);
+
 /* One head slice of a fused projection output, for sa3k_head_prep_{fwd,bwd}. */
 typedef struct sa3k_head_slice {
   int col;              /* first column of the slice in y (a multiple of 64)               */

@@ -9,6 +9,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 namespace sa3k {
@@ -542,6 +543,69 @@ int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim
   }
   float* dsum = static_cast<float*>(scratch_get(&ctx->c, kS_OPT + 1, sizeof(float) * (size_t)B * H * Sq, e));
   if (!dsum) return fill_err(err, err_len, e);
+  a.Dsum = dsum;
+  if (attn_backward(&ctx->c, a, kv, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
+// ------------------------------------------------------------------ attention backward, fixed scratch
+// The one scratch buffer of the attention backward (D = rowsum(dO o O), one float per (b, h, query
+// row)) lives in this file-scope device array instead of context scratch, so the entry point
+// below never allocates device memory.  Its device address is looked up once per device.
+constexpr int64_t kNoAllocDsumRows = int64_t(1) << 20;           // 4 MiB of f32
+static __device__ __align__(256) float g_noalloc_dsum[kNoAllocDsumRows];
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_dsum_addr[kNoAllocMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+
+int sa3k_attention_bwd_noalloc(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale,
+                               int window, const sa3k_tensor4* q, const sa3k_tensor4* k,
+                               const sa3k_tensor4* v, const sa3k_tensor4* o, const sa3k_tensor4* dO,
+                               const float* lse, const sa3k_tensor4* dq, const sa3k_tensor4* dk,
+                               const sa3k_tensor4* dv, char* err, int err_len) {
+  if (!ctx || !dO || !dq || !lse) return fill_err(err, err_len, "NULL argument");
+  const int dev = ctx->c.device;
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fill_err(err, err_len, "device index out of range");
+  if (B <= 0 || H <= 0 || Sq <= 0) return fill_err(err, err_len, "B, H and Sq must be positive");
+  const int64_t rows = (int64_t)B * H * Sq;
+  if (rows > kNoAllocDsumRows) {
+    char msg[160];
+    std::snprintf(msg, sizeof msg,
+                  "sa3k_attention_bwd_noalloc: B*H*Sq = %lld exceeds its fixed scratch of %lld rows",
+                  (long long)rows, (long long)kNoAllocDsumRows);
+    return fill_err(err, err_len, msg);
+  }
+  if (cudaSetDevice(dev) != cudaSuccess) return fill_err(err, err_len, "cudaSetDevice failed");
+  float* dsum = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_dsum_addr[dev]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_dsum);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fill_err(err, err_len, std::string("cudaGetSymbolAddress of the fixed scratch failed: ") +
+                                          cudaGetErrorString(e));
+      }
+      g_noalloc_dsum_addr[dev] = static_cast<float*>(p);
+    }
+    dsum = g_noalloc_dsum_addr[dev];
+  }
+  std::string e;
+  AttnArgs a;
+  if (attn_args(B, H, Sq, Sk, head_dim, scale, window, q, k, v, o, a, e)) return fill_err(err, err_len, e);
+  a.lse = const_cast<float*>(lse);
+  set4(dO, a.dO, a.dO_sb, a.dO_sh, a.dO_ld);
+  a.dq = static_cast<float*>(dq->data); a.dq_sb = (long)dq->batch_stride; a.dq_sh = (long)dq->head_stride;
+  a.dq_ld = (long)dq->row_stride;
+  const bool kv = dk && dv && dk->data && dv->data;
+  if (kv) {
+    a.dk = static_cast<float*>(dk->data); a.dk_sb = (long)dk->batch_stride; a.dk_sh = (long)dk->head_stride;
+    a.dk_ld = (long)dk->row_stride;
+    a.dv = static_cast<float*>(dv->data); a.dv_sb = (long)dv->batch_stride; a.dv_sh = (long)dv->head_stride;
+    a.dv_ld = (long)dv->row_stride;
+  }
+  // every D entry is written by the pre-pass before the dq / dk-dv passes read it: no clearing
   a.Dsum = dsum;
   if (attn_backward(&ctx->c, a, kv, e)) return fill_err(err, err_len, e);
   return 0;

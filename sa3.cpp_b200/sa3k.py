@@ -20,7 +20,7 @@ ABI_SYMBOLS = (
     "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_linear_fwd",
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
-    "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
+    "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_attention_bwd_noalloc", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
     "sa3k_dit_create", "sa3k_dit_free", "sa3k_dit_set_tensor", "sa3k_dit_init_adapters", "sa3k_dit_adapter_size",
     "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
     "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw",
@@ -113,6 +113,7 @@ def lib():
         T4 = ctypes.POINTER(Tensor4)
         L.sa3k_attention_fwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, P, E, I]
         L.sa3k_attention_bwd.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, T4, P, T4, T4, T4, E, I]
+        L.sa3k_attention_bwd_noalloc.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, T4, P, T4, T4, T4, E, I]
         L.sa3k_head_prep_fwd.argtypes = [P, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, I, F, P, E, I]
         L.sa3k_head_prep_bwd.argtypes = [P, P, I64, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, P, E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
@@ -202,6 +203,14 @@ class Context:
                                         ctypes.byref(v), ctypes.byref(o), ctypes.byref(dO), _ptr(lse), ctypes.byref(dq),
                                         ctypes.byref(dk) if dk else None, ctypes.byref(dv) if dv else None, err, 512),
                err)
+
+    def attention_bwd_noalloc(self, B, H, Sq, Sk, scale, window, q, k, v, o, dO, lse, dq, dk=None, dv=None):
+        """attention_bwd with its scratch in a fixed library array (B*H*Sq <= 2**20); see sa3k.h."""
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_attention_bwd_noalloc(self._h, B, H, Sq, Sk, 64, scale, window, ctypes.byref(q),
+                                                ctypes.byref(k), ctypes.byref(v), ctypes.byref(o), ctypes.byref(dO),
+                                                _ptr(lse), ctypes.byref(dq), ctypes.byref(dk) if dk else None,
+                                                ctypes.byref(dv) if dv else None, err, 512), err)
 
     def head_prep_fwd(self, y, T, ncols, H, slices, tps, eps, rot, base, out):
         err = ctypes.create_string_buffer(512)
