@@ -561,13 +561,6 @@ def graph_kernel_nodes(g):
         return {"unavailable": str(e)[:120]}
 
 
-class _DevBuf:
-    """A raw device pointer seen by torch through __cuda_array_interface__ (zero copy)."""
-
-    def __init__(self, ptr, n):
-        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": (n,), "typestr": "<f4", "version": 2}
-
-
 def main_dit(args):
     import torch
     import torch.distributed as dist
@@ -585,7 +578,11 @@ def main_dit(args):
     B, T, C = DIT_B, DIT_T, DIT_CTX
     ctx = sa3k.Context(local)
     dit = build_dit(ctx, cfg, seed=1234)                 # identical base + adapters on every rank
-    grads = torch.as_tensor(_DevBuf(dit.buffer_ptr(1), dit.size()), device=dev)
+    comm = None
+    if world > 1:   # the library's own NCCL clique for the gradient all-reduce (sa3k_dp_*)
+        import dp
+        uid = dp.exchange_unique_id(rank, sa3k.dp_unique_id, dist.broadcast_object_list)
+        comm = sa3k.DpComm(ctx, world, rank, uid)
     hp = sa3k.AdamWParams(1e-4, 0.9, 0.999, 1e-8, 0.01, 1.0)
     host_in = dit_inputs(cfg, B, seed=100 + rank)       # each rank its own samples
     dev_in = [torch.from_numpy(a).to(dev) for a in host_in]
@@ -596,12 +593,14 @@ def main_dit(args):
     def fwd_bwd(inputs, loss):
         dit.zero_grads()
         dit.forward_backward(B, T, C, *inputs, loss=loss)
-        if world > 1:
-            dist.all_reduce(grads)
 
     def adam():
+        """All-reduce of the flat gradients over the ranks + averaged, clipped AdamW (one call)."""
         state["step"] += 1
-        dit.apply_adamw(B * world, hp, state["step"])
+        if comm is not None:
+            dit.dp_apply_adamw(comm, B, hp, state["step"])
+        else:
+            dit.apply_adamw(B, hp, state["step"])
 
     def capture(timing, inputs, loss):
         ctx.profile_enable(timing=timing)
@@ -724,10 +723,14 @@ def main_dit(args):
             "graph_kernel_nodes": nodes,
             "clocks": clk.summary(),
             "loss": loss_now,
-            "graph": "fwd+bwd (+all-reduce) replayed from a CUDA graph; AdamW launched eagerly per step",
+            "graph": "fwd+bwd replayed from a CUDA graph; gradient all-reduce (NCCL, N > 1) + AdamW launched "
+                     "eagerly per step through sa3k_dit_dp_apply_adamw / sa3k_dit_apply_adamw",
             "kernels": {k: {"launches": v[0], "ms_per_step": round(v[1] / kprof, 4)} for k, v in sorted(prof.items())},
         }
         print(json.dumps(line), flush=True)
+    ctx.sync()
+    if comm is not None:
+        comm.close()
     dit.close()
     if world > 1:
         dist.barrier()

@@ -295,6 +295,35 @@ int sa3k_dit_forward_backward(sa3k_dit* dit, int B, int T, int ctx_len, const fl
 int sa3k_dit_apply_adamw(sa3k_dit* dit, int count, const sa3k_adamw_params* hp, int step,
                          double* grad_norm_out, char* err, int err_len);
 
+/* ---------------------------------------------------------------- data parallel (NCCL)
+ * One process per GPU.  The reference trains on one device and sums per-sample gradients on the
+ * host (src/train_loop.h:84-134) before train_average_and_clip (src/train_loop.h:147-171); over
+ * ranks that sum becomes an all-reduce and the average divides by samples-per-rank x ranks, so
+ * every rank applies the identical AdamW update.  NCCL is loaded at run time (libnccl.so.2, or
+ * the path in SA3K_NCCL_LIBRARY); without it these calls return an error. */
+typedef struct sa3k_dp_comm sa3k_dp_comm;
+
+/* 128 opaque bytes made on one rank and handed to every rank (by the caller's own means). */
+int sa3k_dp_unique_id(void* out, int out_len, char* err, int err_len);
+/* Collective over all nranks processes (each with its own context / device). */
+int sa3k_dp_comm_create(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id,
+                        sa3k_dp_comm** out, char* err, int err_len);
+void sa3k_dp_comm_destroy(sa3k_dp_comm* comm);
+int sa3k_dp_comm_info(const sa3k_dp_comm* comm, int* nranks, int* rank);
+/* In-place sum of buf[n] (f32, device) over all ranks, on the context's stream. */
+int sa3k_dp_allreduce_sum(sa3k_ctx* ctx, sa3k_dp_comm* comm, float* buf, int64_t n, char* err,
+                          int err_len);
+/* All-reduce g, then sa3k_average_clip_adamw with count = samples_per_rank x nranks: the
+ * data-parallel form of train_apply_accumulated_adamw (src/train_loop.h:173-211). */
+int sa3k_dp_allreduce_adamw(sa3k_ctx* ctx, sa3k_dp_comm* comm, float* p, float* g, float* m,
+                            float* v, int64_t n, int samples_per_rank,
+                            const sa3k_adamw_params* hp, int step, double* grad_norm_out,
+                            char* err, int err_len);
+/* sa3k_dp_allreduce_adamw on a DiT's flat adapter state. */
+int sa3k_dit_dp_apply_adamw(sa3k_dit* dit, sa3k_dp_comm* comm, int samples_per_rank,
+                            const sa3k_adamw_params* hp, int step, double* grad_norm_out,
+                            char* err, int err_len);
+
 #ifdef __cplusplus
 }
 #endif

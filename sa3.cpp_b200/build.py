@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", os.path.join(os.path.dirname(HERE), "include")]
-SOURCES = ["quant.cu", "gemm_tc.cu", "lora.cu", "adamw.cu", "attention.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu"]
+SOURCES = ["quant.cu", "gemm_tc.cu", "lora.cu", "adamw.cu", "attention.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu", "dp.cu"]
 
 
 def _compile(src, verbose):
@@ -51,7 +51,7 @@ def build(verbose=False):
     out = os.path.join(LIB, "libsa3k.so")
     objs = [o for o, _ in results]
     if not os.path.exists(out) or os.path.getmtime(out) < max(os.path.getmtime(o) for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", out, *objs]
+        cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", out, *objs, "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -629,4 +629,12 @@ int sa3k_dit_apply_adamw(sa3k_dit* d, int count, const sa3k_adamw_params* hp, in
   return sa3k_average_clip_adamw(m.handle, m.p, m.g, m.am, m.av, m.np, count, hp, step, grad_norm_out, err, err_len);
 }
 
+int sa3k_dit_dp_apply_adamw(sa3k_dit* d, sa3k_dp_comm* comm, int samples_per_rank, const sa3k_adamw_params* hp,
+                            int step, double* grad_norm_out, char* err, int err_len) {
+  if (!d || !comm) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  return sa3k_dp_allreduce_adamw(m.handle, comm, m.p, m.g, m.am, m.av, m.np, samples_per_rank, hp, step,
+                                 grad_norm_out, err, err_len);
+}
+
 }  // extern "C"

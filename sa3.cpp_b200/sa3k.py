@@ -23,7 +23,9 @@ ABI_SYMBOLS = (
     "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_attention_bwd_noalloc", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
     "sa3k_dit_create", "sa3k_dit_free", "sa3k_dit_set_tensor", "sa3k_dit_init_adapters", "sa3k_dit_adapter_size",
     "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
-    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw",
+    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create",
+    "sa3k_dp_comm_destroy", "sa3k_dp_comm_info", "sa3k_dp_allreduce_sum", "sa3k_dp_allreduce_adamw",
+    "sa3k_dit_dp_apply_adamw",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N = 1, 2, 3
 
@@ -116,9 +118,20 @@ def lib():
         L.sa3k_attention_bwd_noalloc.argtypes = [P, I, I, I, I, I, F, I, T4, T4, T4, T4, T4, P, T4, T4, T4, E, I]
         L.sa3k_head_prep_fwd.argtypes = [P, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, I, F, P, E, I]
         L.sa3k_head_prep_bwd.argtypes = [P, P, I64, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, P, E, I]
+        L.sa3k_dp_unique_id.argtypes = [P, I, E, I]
+        L.sa3k_dp_comm_create.argtypes = [P, I, I, P, ctypes.POINTER(P), E, I]
+        L.sa3k_dp_comm_destroy.argtypes = [P]
+        L.sa3k_dp_comm_destroy.restype = None
+        L.sa3k_dp_comm_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.sa3k_dp_allreduce_sum.argtypes = [P, P, P, I64, E, I]
+        L.sa3k_dp_allreduce_adamw.argtypes = [P, P, P, P, P, P, I64, I, ctypes.POINTER(AdamWParams), I,
+                                              ctypes.POINTER(ctypes.c_double), E, I]
+        L.sa3k_dit_dp_apply_adamw.argtypes = [P, P, I, ctypes.POINTER(AdamWParams), I,
+                                              ctypes.POINTER(ctypes.c_double), E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
-            if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free", "sa3k_dit_free"):
+            if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free", "sa3k_dit_free",
+                            "sa3k_dp_comm_destroy"):
                 getattr(L, name).restype = I
         L.sa3k_dit_adapter_size.restype = I64
         _lib = L
@@ -364,9 +377,63 @@ class Dit:
         _check(lib().sa3k_dit_forward_backward(self._h, B, T, ctx_len, _ptr(x_t), _ptr(target), _ptr(t_feat),
                                                _ptr(cross), _ptr(glob), _ptr(loss), err, 1024), err)
 
+    def dp_apply_adamw(self, comm, samples_per_rank, hp, step, want_norm=False):
+        """All-reduce the gradients over comm's ranks, then AdamW with count = samples_per_rank x ranks."""
+        err = ctypes.create_string_buffer(512)
+        norm = ctypes.c_double(0.0)
+        _check(lib().sa3k_dit_dp_apply_adamw(self._h, comm._h, samples_per_rank, ctypes.byref(hp), step,
+                                             ctypes.byref(norm) if want_norm else None, err, 512), err)
+        return norm.value if want_norm else None
+
     def apply_adamw(self, count, hp, step, want_norm=False):
         err = ctypes.create_string_buffer(512)
         norm = ctypes.c_double(0.0)
         _check(lib().sa3k_dit_apply_adamw(self._h, count, ctypes.byref(hp), step,
                                           ctypes.byref(norm) if want_norm else None, err, 512), err)
         return norm.value if want_norm else None
+
+
+# ------------------------------------------------------------------------ data parallel
+def dp_unique_id():
+    """128 bytes identifying a new NCCL clique (make on one rank, hand to all)."""
+    buf = ctypes.create_string_buffer(128)
+    err = ctypes.create_string_buffer(512)
+    _check(lib().sa3k_dp_unique_id(buf, 128, err, 512), err)
+    return buf.raw
+
+
+class DpComm:
+    """A data-parallel communicator of nranks processes, one per GPU (sa3k_dp_comm_*)."""
+
+    def __init__(self, ctx, nranks, rank, unique_id):
+        assert len(unique_id) == 128
+        self.ctx = ctx
+        self._h = ctypes.c_void_p()
+        uid = ctypes.create_string_buffer(bytes(unique_id), 128)
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dp_comm_create(ctx._h, nranks, rank, uid, ctypes.byref(self._h), err, 512), err)
+        self.nranks, self.rank = nranks, rank
+
+    def allreduce_sum(self, buf, n=None):
+        n = buf.numel() if n is None else n
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dp_allreduce_sum(self.ctx._h, self._h, _ptr(buf), n, err, 512), err)
+
+    def allreduce_adamw(self, p, g, m, v, samples_per_rank, hp, step, want_norm=False):
+        err = ctypes.create_string_buffer(512)
+        norm = ctypes.c_double(0.0)
+        _check(lib().sa3k_dp_allreduce_adamw(self.ctx._h, self._h, _ptr(p), _ptr(g), _ptr(m), _ptr(v), p.numel(),
+                                             samples_per_rank, ctypes.byref(hp), step,
+                                             ctypes.byref(norm) if want_norm else None, err, 512), err)
+        return norm.value if want_norm else None
+
+    def close(self):
+        if self._h:
+            lib().sa3k_dp_comm_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
