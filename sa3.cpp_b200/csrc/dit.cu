@@ -53,6 +53,7 @@ struct DitBlockAct {
 struct DitModel {
   Ctx* c = nullptr;
   sa3k_ctx* handle = nullptr;
+  int device = 0;
   sa3k_dit_config cfg{};
   std::map<std::string, Weight*> W;
   std::vector<sa3k_weight*> weights;   // owned weight handles (W points into them)
@@ -458,6 +459,7 @@ int sa3k_dit_create(sa3k_ctx* ctx, const sa3k_dit_config* cfg, sa3k_dit** out, c
   if (!d) return dfail(err, err_len, "out of host memory");
   d->m.c = &ctx->c;
   d->m.handle = ctx;
+  d->m.device = ctx->c.device;
   d->m.cfg = *cfg;
   *out = d;
   return 0;
@@ -465,8 +467,9 @@ int sa3k_dit_create(sa3k_ctx* ctx, const sa3k_dit_config* cfg, sa3k_dit** out, c
 
 void sa3k_dit_free(sa3k_dit* d) {
   if (!d) return;
-  cudaSetDevice(d->m.c->device);
-  cudaStreamSynchronize(d->m.c->stream);
+  // the model's context may already be gone: use the device recorded at creation only
+  // (cudaFree waits for the device's outstanding work)
+  cudaSetDevice(d->m.device);
   delete d;
 }
 

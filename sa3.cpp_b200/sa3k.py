@@ -7,6 +7,7 @@ computation runs in libsa3k's own kernels).  The library must have been built in
 from __future__ import annotations
 
 import ctypes
+import weakref
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -178,7 +179,15 @@ class Context:
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_sync(self._h, err, 512), err)
 
+    def _own(self, obj):
+        """Objects made on this context (weights, models, communicators) are released before it."""
+        if not hasattr(self, "_children"):
+            self._children = weakref.WeakSet()
+        self._children.add(obj)
+
     def close(self):
+        for obj in list(getattr(self, "_children", ())):
+            obj.close()
         if self._h:
             lib().sa3k_ctx_destroy(self._h)
             self._h = ctypes.c_void_p()
@@ -301,11 +310,14 @@ class Context:
 class Weight:
     def __init__(self, ctx, h, qtype, inn, out):
         self.ctx, self._h, self.qtype, self.inn, self.out = ctx, h, qtype, inn, out
+        ctx._own(self)
 
     def free(self):
         if self._h:
             lib().sa3k_weight_free(self._h)
             self._h = ctypes.c_void_p()
+
+    close = free
 
     def __del__(self):
         try:
@@ -323,6 +335,7 @@ class Dit:
         self._h = ctypes.c_void_p()
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_dit_create(ctx._h, ctypes.byref(c), ctypes.byref(self._h), err, 512), err)
+        ctx._own(self)
 
     def close(self):
         if self._h:
@@ -413,6 +426,7 @@ class DpComm:
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_dp_comm_create(ctx._h, nranks, rank, uid, ctypes.byref(self._h), err, 512), err)
         self.nranks, self.rank = nranks, rank
+        ctx._own(self)
 
     def allreduce_sum(self, buf, n=None):
         n = buf.numel() if n is None else n

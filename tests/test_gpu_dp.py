@@ -95,7 +95,10 @@ def test_two_gpu_dp_step_matches_one_gpu(ctx):
     p1 = np.zeros(dit.size(), np.float32)
     dit.copy(0, p1, to_model=False)
     ctx.sync()
-    np.testing.assert_allclose(r0["norms"], norms, rtol=1e-4)
+    # step 1 sees identical adapters (norms agree to f32 summation order); step 2 sees adapters
+    # whose AdamW updates already differ slightly, so its gradient norm is compared loosely
+    np.testing.assert_allclose(r0["norms"][0], norms[0], rtol=1e-4)
+    np.testing.assert_allclose(r0["norms"][1:], norms[1:], rtol=2e-3)
     upd_dp, upd_one = r0["p"] - p0, p1 - p0
     rel = np.linalg.norm(upd_dp - upd_one) / np.linalg.norm(upd_one)
     assert rel < 1e-2, rel
