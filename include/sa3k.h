@@ -59,6 +59,10 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
 /* SA3K_OPT_GEMM_TILE_N  0 (default): the N tile of the large GEMMs comes from a wave-count cost
  *       model; 128 or 256 fixes it (a tuning knob; results do not depend on it). */
 #define SA3K_OPT_GEMM_TILE_N 3
+/* SA3K_OPT_GEMM_PAIR  1 (default): bf16-operand GEMMs with at least 256 rows and enough output
+ *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always.
+ *       Results are identical either way (same per-element summation order). */
+#define SA3K_OPT_GEMM_PAIR 4
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded

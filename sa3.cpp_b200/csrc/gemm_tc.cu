@@ -1,5 +1,6 @@
 // gemm_tc.cu -- host side of the tcgen05 GEMM engine: tensor maps, tile choice, launch.
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "sa3k_internal.h"
 
 #include <cstdio>
@@ -114,6 +115,66 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   return 0;
 }
 
+// CTA-pair launch (cta_group::2, clusters of 2): bf16 operands, no split-K.
+template <int BN, int STAGES, int BMODE>
+static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtensorMap& tb,
+                       const CUtensorMap& tea, const CUtensorMap& teb, const GemmArgs& args, std::string& err) {
+  using L = Gemm2Smem<BN, STAGES>;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  auto kern = gemm_tc2_kernel<BN, STAGES, BMODE>;
+  static int max_clusters = 0;
+  if (!max_clusters) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN) != cudaSuccess)
+      return check_launch("gemm pair smem attribute", err);
+    cudaLaunchConfig_t q = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+    q.gridDim = dim3(2 * (unsigned)(c->sm_count / 2));
+    q.blockDim = dim3(192);
+    q.dynamicSmemBytes = L::DYN;
+    q.attrs = at;
+    q.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = c->sm_count / 2;
+    }
+    max_clusters = n;
+  }
+  GemmArgs a = args;
+  a.splits = 1;
+  a.kb_per_split = (d.K + kBK - 1) / kBK;
+  a.partial = nullptr;
+  CUtensorMap tout = ta;
+  a.tma_out = 0;
+  {
+    std::string e2;
+    if (d.out && !d.out_bf && !d.out_trans && (d.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
+        !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d.out, d.N, d.M, d.ldo * 4, 32, 32, SW, "out", e2))
+      a.tma_out = 1;
+    else if (d.out_bf && !d.out && !d.out_bf_trans && (d.ldo_bf % 8) == 0 &&
+             (reinterpret_cast<uintptr_t>(d.out_bf) & 15) == 0 &&
+             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
+      a.tma_out = 2;
+  }
+  const long tiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + BN - 1) / BN);
+  const long clusters = tiles < (long)max_clusters ? tiles : (long)max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = L::DYN;
+  cfg.stream = c->stream;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  ProfScope prof_(c, d.name);
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tea, teb, tout, a) != cudaSuccess) return check_launch("gemm_tc2", err);
+  return check_launch("gemm_tc2", err);
+}
+
 // N tile for the main GEMMs: the cheaper of 128 / 256 by a wave-quantized cost model.
 static int pick_bn(const Ctx* c, int M, int N) {
   if (N <= 128) return 128;
@@ -122,6 +183,18 @@ static int pick_bn(const Ctx* c, int M, int N) {
     const long tiles = tm * ((N + bn - 1) / bn);
     const long waves = (tiles + (long)c->sm_count - 1) / (long)c->sm_count;
     return waves * (bn + 24);   // + per-tile overhead (prologue / epilogue tail)
+  };
+  return cost(256) <= cost(128) ? 256 : 128;
+}
+
+// N tile of a CTA-pair GEMM (256-row pair tiles over the clusters that fit the GPU).
+static int pick_bn_pair(const Ctx* c, int M, int N) {
+  const long tm = (M + 2 * kBM - 1) / (2 * kBM);
+  const long slots = c->sm_count / 2;
+  auto cost = [&](int bn) {
+    const long tiles = tm * ((N + bn - 1) / bn);
+    const long waves = (tiles + slots - 1) / slots;
+    return waves * (bn + 24);
   };
   return cost(256) <= cost(128) ? 256 : 128;
 }
@@ -229,6 +302,28 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
                   : launch<16, 8, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
   }
   if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
+  // CTA pairs for the bf16-operand GEMMs with enough output tiles to fill the GPU without split-K
+  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM) {
+    const long tiles1 = (long)((d.M + kBM - 1) / kBM) * ((d.N + bn - 1) / bn);
+    if (tiles1 * 2 > (long)c->sm_count) {
+      const int bp = (d.N <= 128 || c->tile_n == 128) ? 128 : pick_bn_pair(c, d.M, d.N);
+      CUtensorMap tb2 = tb, tea2 = tea, teb2 = teb;
+      // B halves: BN/2 rows (K-major) per CTA; MN-major B keeps its 64-wide atoms
+      if (bmode == 0) {
+        const void* bptr = d.bsrc == kB_BF16_KMAJOR ? d.b : d.w->bf16;
+        const long bk = d.bsrc == kB_BF16_KMAJOR ? d.K : d.w->in;
+        const long bld = d.bsrc == kB_BF16_KMAJOR ? d.ldb * 2 : d.w->in * 2;
+        if (make_map(&tb2, BF, bptr, bk, d.N, bld, 64, bp / 2, SW, "B half", err)) return 1;
+      }
+      if (d.ext_a) {
+        if (make_map(&teb2, BF, d.ext_b, 64, d.N, 128, 64, bp / 2, SW, "ext B half", err)) return 1;
+      }
+      if (bp == 256) return bmode == 0 ? launch_pair<256, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err)
+                                       : launch_pair<256, 6, 1>(c, d, ta, tb2, tea2, teb2, a, err);
+      return bmode == 0 ? launch_pair<128, 8, 0>(c, d, ta, tb2, tea2, teb2, a, err)
+                        : launch_pair<128, 8, 1>(c, d, ta, tb2, tea2, teb2, a, err);
+    }
+  }
   if (bn == 256) {
     switch (bmode) {
       case 0: return launch<256, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);

@@ -197,6 +197,41 @@ __global__ void splitk_reduce_kernel(const GemmArgs args) {
   }
 }
 
+// ------------------------------------------------------------------ epilogue arithmetic
+// f[j] = acc[j] * (alpha * col_scale[n0 + j]) + col_bias[n0 + j] for 32 accumulator columns
+// (raw sums for split-K partials).  Column vectors are read 4 at a time (the same addresses for
+// every lane of the warp: broadcast loads).
+__device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, int n0, const GemmArgs& args,
+                                            bool raw) {
+  if (raw || !(args.col_scale || args.col_bias)) {
+    const float al = raw ? 1.f : args.alpha;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * al + 0.f;
+  } else if (n0 + 32 <= args.N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      float4 s4 = make_float4(1.f, 1.f, 1.f, 1.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (args.col_scale) s4 = __ldg(reinterpret_cast<const float4*>(args.col_scale + n0 + j));
+      if (args.col_bias) b4 = __ldg(reinterpret_cast<const float4*>(args.col_bias + n0 + j));
+      f[j] = __uint_as_float(v[j]) * (args.alpha * s4.x) + b4.x;
+      f[j + 1] = __uint_as_float(v[j + 1]) * (args.alpha * s4.y) + b4.y;
+      f[j + 2] = __uint_as_float(v[j + 2]) * (args.alpha * s4.z) + b4.z;
+      f[j + 3] = __uint_as_float(v[j + 3]) * (args.alpha * s4.w) + b4.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const int n = n0 + j;
+      float cs = args.alpha, cb = 0.f;
+      if (n < args.N) {
+        if (args.col_scale) cs *= args.col_scale[n];
+        if (args.col_bias) cb = args.col_bias[n];
+      }
+      f[j] = __uint_as_float(v[j]) * cs + cb;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ the kernel
 // Persistent: gridDim.x CTAs walk the work items blockIdx.x, blockIdx.x + gridDim.x, ...; an item
 // is an output tile t (m-tile t % tiles_m, n-tile t / tiles_m, so co-resident CTAs share B
@@ -415,39 +450,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
           } else {
             tmem_ld16(tacc + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           }
-          // column scale / bias for these 32 columns (uniform across the warp: broadcast loads)
-          float cs[32], cb[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) { cs[j] = args.alpha; cb[j] = 0.f; }
-          if (!split_out && (args.col_scale || args.col_bias) && nb + 32 * h + 32 <= args.N) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (args.col_scale) {
-                const float4 x4 = __ldg(reinterpret_cast<const float4*>(args.col_scale + nb + 32 * h + j));
-                cs[j] *= x4.x; cs[j + 1] *= x4.y; cs[j + 2] *= x4.z; cs[j + 3] *= x4.w;
-              }
-              if (args.col_bias) {
-                const float4 x4 = __ldg(reinterpret_cast<const float4*>(args.col_bias + nb + 32 * h + j));
-                cb[j] = x4.x; cb[j + 1] = x4.y; cb[j + 2] = x4.z; cb[j + 3] = x4.w;
-              }
-            }
-          } else if (!split_out && (args.col_scale || args.col_bias)) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = nb + 32 * h + j;
-              if (n < args.N) {
-                if (args.col_scale) cs[j] *= args.col_scale[n];
-                if (args.col_bias) cb[j] = args.col_bias[n];
-              }
-            }
-          }
-          if (split_out) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) { cs[j] = 1.f; cb[j] = 0.f; }
-          }
           tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) f[32 * h + j] = __uint_as_float(v[j]) * cs[j] + cb[j];
+          epi_columns(v, f + 32 * h, nb + 32 * h, args, split_out);
         }
         if (!have || nb >= args.N) continue;
         if (args.tma_out) {
@@ -491,16 +495,23 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         const int ncols = min(min(32, BN - c0), args.N - nb);
         const int myrow = rbase + lane;
         if (args.out && args.out_trans) {          // lanes are consecutive rows: coalesced
-          if (myrow < args.M)
-            for (int j = 0; j < ncols; ++j) {
+          if (myrow < args.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {   // static indices keep f[] in registers
+              if (j >= ncols) break;
               float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
               *dst = args.accumulate ? *dst + f[j] : f[j];
             }
+          }
         }
         if (args.out_bf && args.out_bf_trans) {
-          if (myrow < args.M)
-            for (int j = 0; j < ncols; ++j)
+          if (myrow < args.M) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j >= ncols) break;
               args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j]);
+            }
+          }
         }
         if (split_out || (args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
           float* st32 = reinterpret_cast<float*>(stg);     // 32 x 32 f32, XOR-swizzled columns

@@ -149,6 +149,48 @@ def test_linear_config2_q4_k_dora(ctx, operand_path):
     assert all(v < TOL for v in res.values()), res
 
 
+def _outputs(ctx, c, qtype, S, inn, out, rank):
+    import torch
+    w = ctx.upload(c["raw"], qtype, inn, out)
+    A, B, m, bns = _dev(c["A"]), _dev(c["B"]), _dev(c["m"]), _dev(c["bns"])
+    ad = ctx.adapter(A, B, 1.0, m, bns)
+    y = torch.empty(S, out, device="cuda")
+    dx = torch.empty(S, inn, device="cuda")
+    dA = torch.empty(rank, inn, device="cuda")
+    dB = torch.empty(out, rank, device="cuda")
+    dm = torch.empty(out, device="cuda")
+    ctx.linear_fwd_bwd(w, _dev(c["x"]), _dev(c["dy"]), y, dx, ad=ad, bias=_dev(c["bias"]), dA=dA, dB=dB, dm=dm)
+    ctx.sync()
+    return {k: v.cpu().numpy() for k, v in dict(y=y, dx=dx, dA=dA, dB=dB, dm=dm).items()}
+
+
+@pytest.mark.parametrize("S,inn,out", [(1000, 2560, 3072), (4352, 1536, 4608)])
+def test_cta_pair_gemms_match_single_cta(ctx, S, inn, out):
+    """The forward and dX GEMMs of these shapes run on CTA pairs (cta_group::2, 256-row tiles) by
+    default; with pairs switched off they run one CTA per 128-row tile.  Both accumulate every
+    output element over K in the same order, so y and dx agree to f32 rounding (and the adapter
+    gradients, fed by them, to the rounding of their atomic column sums)."""
+    import sa3k
+    c = _case("q8_0", S, inn, out, 16, 31)
+    got = {}
+    for pair in (1, 0):
+        ctx.set_option(sa3k.OPT_GEMM_PAIR, pair)
+        got[pair] = _outputs(ctx, c, "q8_0", S, inn, out, 16)
+    ctx.set_option(sa3k.OPT_GEMM_PAIR, 1)
+    for k in ("y", "dx"):
+        assert np.isfinite(got[1][k]).all(), k
+        assert rel_l2(got[1][k], got[0][k]) < 1e-6, k
+    for k in ("dA", "dB", "dm"):
+        assert rel_l2(got[1][k], got[0][k]) < 1e-5, k
+    if S * inn * out <= 1e10:     # oracle check where the float64 restatement stays quick
+        ref_y, cache = oracle.dit_lin_fwd(c["x"], c["Wd"], c["A"], c["B"], 1.0, c["m"], c["bns"], c["bias"])
+        ref = oracle.dit_lin_bwd(c["dy"], cache)
+        res = {"y": rel_l2(got[1]["y"], ref_y), "dx": rel_l2(got[1]["dx"], ref["dx"]),
+               "dA": rel_l2(got[1]["dA"], ref["dA"]), "dB": rel_l2(got[1]["dB"], ref["dB"]),
+               "dm": rel_l2(got[1]["dm"], ref["dm"])}
+        assert all(v < TOL for v in res.values()), res
+
+
 def test_linear_accumulate(ctx):
     import torch
     c = _case("q8_0", 96, 256, 256, 16, 5)
