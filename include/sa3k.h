@@ -57,7 +57,7 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
 #define SA3K_OPT_WEIGHT_BF16_CACHE 1
 #define SA3K_OPT_SMEM_DEQUANT 2
 /* SA3K_OPT_GEMM_TILE_N  0 (default): the N tile of the large GEMMs comes from a wave-count cost
- *       model; 128 or 256 fixes it (a tuning knob; results do not depend on it). */
+ *       model; 128, 192 or 256 fixes it (a tuning knob; results do not depend on it). */
 #define SA3K_OPT_GEMM_TILE_N 3
 /* SA3K_OPT_GEMM_PAIR  1 (default): bf16-operand GEMMs with at least 256 rows and enough output
  *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always.

@@ -256,7 +256,8 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
     case SA3K_OPT_WEIGHT_BF16_CACHE: ctx->c.weight_cache = value != 0; return 0;
     case SA3K_OPT_SMEM_DEQUANT: ctx->c.smem_dequant = value != 0; return 0;
     case SA3K_OPT_GEMM_TILE_N:
-      if (value != 0 && value != 128 && value != 256) return fill_err(err, err_len, "tile N must be 0, 128 or 256");
+      if (value != 0 && value != 128 && value != 192 && value != 256)
+        return fill_err(err, err_len, "tile N must be 0, 128, 192 or 256");
       ctx->c.tile_n = (int)value;
       return 0;
     case SA3K_OPT_GEMM_PAIR: ctx->c.gemm_pair = value != 0; return 0;

@@ -175,28 +175,23 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
   return check_launch("gemm_tc2", err);
 }
 
-// N tile for the main GEMMs: the cheaper of 128 / 256 by a wave-quantized cost model.
-static int pick_bn(const Ctx* c, int M, int N) {
+// N tile for the main GEMMs from a wave-quantized cost model: waves x per-tile time, the time of
+// a 128 x bn tile taken as bn / eff(bn) + a fixed prologue / epilogue share.  eff() is the
+// measured per-tile tensor efficiency of the one-CTA kernel (narrow tiles stream more operand
+// bytes per MMA cycle); quantized B operands have only the 128 / 256 instantiations.
+static int pick_bn(const Ctx* c, int M, int N, bool quant) {
   if (N <= 128) return 128;
   const long tm = (M + kBM - 1) / kBM;
-  auto cost = [&](int bn) {
+  auto cost = [&](int bn, double eff) {
     const long tiles = tm * ((N + bn - 1) / bn);
     const long waves = (tiles + (long)c->sm_count - 1) / (long)c->sm_count;
-    return waves * (bn + 24);   // + per-tile overhead (prologue / epilogue tail)
+    return (double)waves * (bn / eff + 16.0);
   };
-  return cost(256) <= cost(128) ? 256 : 128;
-}
-
-// N tile of a CTA-pair GEMM (256-row pair tiles over the clusters that fit the GPU).
-static int pick_bn_pair(const Ctx* c, int M, int N) {
-  const long tm = (M + 2 * kBM - 1) / (2 * kBM);
-  const long slots = c->sm_count / 2;
-  auto cost = [&](int bn) {
-    const long tiles = tm * ((N + bn - 1) / bn);
-    const long waves = (tiles + slots - 1) / slots;
-    return waves * (bn + 24);
-  };
-  return cost(256) <= cost(128) ? 256 : 128;
+  int best = 256;
+  double bc = cost(256, 1.0);
+  if (!quant && cost(192, 0.90) < bc) { best = 192; bc = cost(192, 0.90); }
+  if (cost(128, 0.72) < bc) best = 128;
+  return best;
 }
 
 int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
@@ -210,8 +205,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
                      !(d.w->bf16 && !c->smem_dequant);
   int bn = d.bn;
-  if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N);
-  if (!(bn == 16 || bn == 128 || bn == 256)) {
+  if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N, quant);
+  if (quant && bn == 192) bn = 256;
+  if (!(bn == 16 || bn == 128 || bn == 192 || bn == 256)) {
     err = "gemm: unsupported N tile";
     return 1;
   }
@@ -303,10 +299,12 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   }
   if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
   // CTA pairs for the bf16-operand GEMMs with enough output tiles to fill the GPU without split-K
-  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM) {
-    const long tiles1 = (long)((d.M + kBM - 1) / kBM) * ((d.N + bn - 1) / bn);
-    if (tiles1 * 2 > (long)c->sm_count) {
-      const int bp = (d.N <= 128 || c->tile_n == 128) ? 128 : pick_bn_pair(c, d.M, d.N);
+  // (measured: pairs win once every cluster gets many 256 x 256 tiles; with few tiles per
+  // cluster the one-CTA kernel with its better-balanced waves is faster)
+  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM && d.N >= 256 && c->tile_n != 128 && c->tile_n != 192) {
+    const long ptiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + 255) / 256);
+    if (ptiles >= 8L * (c->sm_count / 2)) {
+      const int bp = 256;
       CUtensorMap tb2 = tb, tea2 = tea, teb2 = teb;
       // B halves: BN/2 rows (K-major) per CTA; MN-major B keeps its 64-wide atoms
       if (bmode == 0) {
@@ -318,10 +316,8 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       if (d.ext_a) {
         if (make_map(&teb2, BF, d.ext_b, 64, d.N, 128, 64, bp / 2, SW, "ext B half", err)) return 1;
       }
-      if (bp == 256) return bmode == 0 ? launch_pair<256, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err)
-                                       : launch_pair<256, 6, 1>(c, d, ta, tb2, tea2, teb2, a, err);
-      return bmode == 0 ? launch_pair<128, 8, 0>(c, d, ta, tb2, tea2, teb2, a, err)
-                        : launch_pair<128, 8, 1>(c, d, ta, tb2, tea2, teb2, a, err);
+      return bmode == 0 ? launch_pair<256, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err)
+                        : launch_pair<256, 6, 1>(c, d, ta, tb2, tea2, teb2, a, err);
     }
   }
   if (bn == 256) {
@@ -333,6 +329,10 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       case 4: return launch<256, 3, 4, false>(c, d, ta, tb, tbs, tea, teb, a, err);
       default: return launch<256, 3, 5, false>(c, d, ta, tb, tbs, tea, teb, a, err);
     }
+  }
+  if (bn == 192) {
+    if (bmode == 0) return launch<192, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
+    return launch<192, 4, 1, false>(c, d, ta, tb, tbs, tea, teb, a, err);
   }
   switch (bmode) {
     case 0: return launch<128, 6, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);

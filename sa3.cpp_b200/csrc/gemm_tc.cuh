@@ -100,9 +100,10 @@ struct GemmSmem {
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
   static constexpr int DYN = TOTAL + 1024;   // slack for 1024-byte alignment of the base
   static constexpr int ACC_COLS = BN < 32 ? 32 : BN;           // one accumulator buffer
-  static constexpr int TMEM_COLS = 2 * ACC_COLS;               // double-buffered
-  static_assert(TMEM_COLS == 64 || TMEM_COLS == 256 || TMEM_COLS == 512 || TMEM_COLS == 128,
-                "TMEM allocation must be a power of two >= 32");
+  // double-buffered; the allocation is a power of two >= 32 columns
+  static constexpr int TMEM_COLS = 2 * ACC_COLS <= 64 ? 64 : 2 * ACC_COLS <= 128 ? 128
+                                 : 2 * ACC_COLS <= 256 ? 256 : 512;
+  static_assert(2 * ACC_COLS <= 512, "two accumulators must fit the 512 TMEM columns");
   static_assert(DYN <= 232448, "shared memory budget (227 KB)");
 };
 
