@@ -63,6 +63,10 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always.
  *       Results are identical either way (same per-element summation order). */
 #define SA3K_OPT_GEMM_PAIR 4
+/* SA3K_OPT_ATTN_TC  1 (default): attention on the tcgen05 tensor cores (TMEM accumulators, P and
+ *       dS fed back from TMEM); 0: the mma.sync kernels.  Both compute in bf16 with f32
+ *       accumulation; results agree to rounding. */
+#define SA3K_OPT_ATTN_TC 5
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded

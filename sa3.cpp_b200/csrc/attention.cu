@@ -427,6 +427,7 @@ static int set_attrs(std::string& err) {
 
 int attn_forward(Ctx* c, const AttnArgs& a, std::string& err) {
   if (a.head_dim != HD) { err = "attention: head_dim must be 64"; return 1; }
+  if (c->attn_tc && attn_tc_supported(a)) return attn_tc_forward(c, a, err);
   if (set_attrs(err)) return 1;
   ProfScope prof_(c, "attn.fwd");
   dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));
@@ -443,6 +444,7 @@ int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err) {
     attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, c->stream>>>(a);
     if (check_launch("attn bwd pre", err)) return 1;
   }
+  if (c->attn_tc && attn_tc_supported(a)) return attn_tc_grads(c, a, want_dkdv, err);
   {
     ProfScope prof_(c, "attn.bwd_dq");
     dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));

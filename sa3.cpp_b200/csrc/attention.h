@@ -24,6 +24,11 @@ struct AttnArgs {
 };
 
 int attn_forward(Ctx* c, const AttnArgs& a, std::string& err);
+// tcgen05 kernels (attention_tc.cu): used by attn_forward / attn_backward when the context allows
+// them and the layout qualifies (16-byte aligned rows and strides)
+bool attn_tc_supported(const AttnArgs& a);
+int attn_tc_forward(Ctx* c, const AttnArgs& a, std::string& err);
+int attn_tc_grads(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err);
 // dq always; dk / dv when want_dkdv (cross-attention to a frozen context needs only dq)
 int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err);
 

@@ -58,6 +58,7 @@ struct Ctx {
   bool smem_dequant = false;         // force the in-smem dequant GEMM path for quantized weights
   int tile_n = 0;                    // main-GEMM N tile: 0 = cost model, 128 or 256 = fixed
   bool gemm_pair = true;             // CTA-pair (cta_group::2) GEMMs where they fit
+  bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
   std::vector<ProfEntry> prof;
   std::vector<cudaEvent_t> ev_pool;
 };

@@ -15,6 +15,15 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-2
 
 
+@pytest.fixture(autouse=True, params=["tcgen05", "mma_sync"])
+def attn_path(request, ctx):
+    """Every test runs on both attention kernel families (SA3K_OPT_ATTN_TC)."""
+    import sa3k
+    ctx.set_option(sa3k.OPT_ATTN_TC, 1 if request.param == "tcgen05" else 0)
+    yield request.param
+    ctx.set_option(sa3k.OPT_ATTN_TC, 1)
+
+
 def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
