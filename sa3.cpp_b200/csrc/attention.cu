@@ -437,6 +437,8 @@ int attn_forward(Ctx* c, const AttnArgs& a, std::string& err) {
 
 int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err) {
   if (a.head_dim != HD) { err = "attention: head_dim must be 64"; return 1; }
+  // the tcgen05 dq pass forms D = rowsum(dO o O) itself
+  if (c->attn_tc && attn_tc_supported(a)) return attn_tc_grads(c, a, want_dkdv, err);
   if (set_attrs(err)) return 1;
   {
     ProfScope prof_(c, "attn.bwd_pre");
@@ -444,7 +446,6 @@ int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err) {
     attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, c->stream>>>(a);
     if (check_launch("attn bwd pre", err)) return 1;
   }
-  if (c->attn_tc && attn_tc_supported(a)) return attn_tc_grads(c, a, want_dkdv, err);
   {
     ProfScope prof_(c, "attn.bwd_dq");
     dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));
