@@ -738,18 +738,108 @@ def main_dit(args):
     return 0
 
 
+# =============================================================================== attention workload
+ATT_B, ATT_H, ATT_S, ATT_W, ATT_C, ATT_COND = 2, 24, 2048, 256, 128, 768
+ATT_WORKLOAD = ("config3: banded self-attention B 2, 24 heads x 64, 2048 frames, window +-256, and cross-attention "
+                "to 128 conditioning tokens (768 -> 1536 frozen K/V projections, done outside the timed step); "
+                "forward + backward (O, dQ, dK, dV of both), bf16 operands, f32 accumulation")
+
+
+def attention_flops(B, H, S, W, C):
+    """Algorithmic FLOPs: 2 (fwd) + 5 (bwd) matmuls of 2 * 64 FLOPs per visible (query, key) pair."""
+    vis = sum(min(S - 1, i + W) - max(0, i - W) + 1 for i in range(S))
+    return 7 * 2 * 64 * (vis + S * C) * B * H
+
+
+def main_attention(args):
+    import torch
+    import sa3k
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and rank != 0:
+        return 0          # a single-GPU component benchmark
+    torch.cuda.set_device(local)
+    B, H, S, W, C = ATT_B, ATT_H, ATT_S, ATT_W, ATT_C
+    D = H * 64
+    ctx = sa3k.Context(local)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    bf = lambda *sh: torch.randn(*sh, generator=g, device="cuda").to(torch.bfloat16)
+    q, k, v, dO = bf(B, S, D), bf(B, S, D), bf(B, S, D), bf(B, S, D)
+    cond = torch.randn(B, C, ATT_COND, generator=g, device="cuda")
+    wk = torch.randn(D, ATT_COND, generator=g, device="cuda") * 0.02
+    wv = torch.randn(D, ATT_COND, generator=g, device="cuda") * 0.02
+    ck, cv = (cond @ wk.t()).to(torch.bfloat16), (cond @ wv.t()).to(torch.bfloat16)
+    o, oc = torch.empty_like(q), torch.empty_like(q)
+    lse, lsec = torch.empty(B * H * S, device="cuda"), torch.empty(B * H * S, device="cuda")
+    f32 = lambda *sh: torch.empty(*sh, device="cuda")
+    dq, dk, dv = f32(B, S, D), f32(B, S, D), f32(B, S, D)
+    dqc, dkc, dvc = f32(B, S, D), f32(B, C, D), f32(B, C, D)
+    T4 = sa3k.t4
+    ts, tc = (S * D, 64, D), (C * D, 64, D)
+    scale = 1.0 / 8.0
+
+    def step():
+        ctx.attention_fwd(B, H, S, S, scale, W, T4(q, *ts), T4(k, *ts), T4(v, *ts), T4(o, *ts), lse)
+        ctx.attention_fwd(B, H, S, C, scale, -1, T4(q, *ts), T4(ck, *tc), T4(cv, *tc), T4(oc, *ts), lsec)
+        ctx.attention_bwd(B, H, S, S, scale, W, T4(q, *ts), T4(k, *ts), T4(v, *ts), T4(o, *ts), T4(dO, *ts), lse,
+                          T4(dq, *ts), T4(dk, *ts), T4(dv, *ts))
+        ctx.attention_bwd(B, H, S, C, scale, -1, T4(q, *ts), T4(ck, *tc), T4(cv, *tc), T4(oc, *ts), T4(dO, *ts),
+                          lsec, T4(dqc, *ts), T4(dkc, *tc), T4(dvc, *tc))
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    flush = torch.empty(256 * 1024 * 1024 // 4, device="cuda")
+    ctx.profile_enable(timing=1)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    total = 0.0
+    with Clocks(local) as clk:
+        for _ in range(args.steps):
+            flush.zero_()
+            e0.record()
+            step()
+            e1.record()
+            torch.cuda.synchronize()
+            total += e0.elapsed_time(e1)
+    prof = ctx.profile_read()
+    ctx.sync()
+    flops = attention_flops(B, H, S, W, C)
+    ms = total / args.steps
+    peak_tf, _, peak_kind = load_peaks()
+    kern_ms = sum(v[1] for n, v in prof.items() if n.startswith("attn")) / args.steps
+    line = {"metric": "attention fwd+bwd TFLOP/s (BASELINE config 3)", "value": flops / (ms / 1e3) / 1e12,
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": ATT_WORKLOAD, "l2": "256 MB flush between timed steps"},
+            "roofline": {"bound": "tensor", "achieved": flops / (kern_ms / 1e3) / 1e12, "peak": peak_tf,
+                         "unit": "TFLOP/s", "frac": flops / (kern_ms / 1e3) / 1e12 / peak_tf, "traffic": None,
+                         "peak_kind": f"{peak_kind} bf16 burst", "algorithmic_gflop": flops / 1e9,
+                         "kernel": "attention kernels (sum of their event-timed launches)"},
+            "clocks": clk.summary(),
+            "kernels": {n: {"launches": v[0], "ms_per_step": round(v[1] / args.steps, 4)} for n, v in sorted(prof.items())}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "linear"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "linear", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "linear":
         return run_linear_reference(args) if args.impl == "reference" else main_linear(args)
+    if args.workload == "attention":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "component workload: the reference arm runs the "
+                                                                   "DiT step (--workload dit)"}))
+            return 0
+        return main_attention(args)
     return run_dit_reference(args) if args.impl == "reference" else main_dit(args)
 
 

@@ -32,7 +32,7 @@ struct TcArgs {
   int B, H, Sq, Sk, window;
   float sl2;                 // scale * log2(e)
   float scale;
-  int q_tm, k_tm, v_tm, o_tm, do_tm;   // tensor-map coordinate order: 1 = (d, h, s, b), 0 = (d, s, h, b)
+  int q_tm, k_tm, v_tm, o_tm, do_tm, dq_tm;   // tensor-map coordinate order: 1 = (d, h, s, b), 0 = (d, s, h, b)
   __nv_bfloat16* o; long o_sb, o_sh, o_ld;
   float* lse;                // forward output [B*H][Sq]
   const float* lse_in;       // backward input
@@ -53,22 +53,18 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* m, uin
       : "memory");
 }
 
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* m, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // rows [row0, row0 + n) of head h of batch b (map coordinate order per `tm`)
 __device__ __forceinline__ void load_rows(void* dst, const CUtensorMap* m, uint64_t* bar, int tm, int b, int h,
                                           int row0) {
   if (tm) tma_load_4d(dst, m, bar, 0, h, row0, b);
   else tma_load_4d(dst, m, bar, 0, row0, h, b);
-}
-
-// D (tmem) (+)= A (tmem, bf16 packed two per column) * B (smem descriptor)
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
@@ -113,6 +109,22 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// max of 64 values held as raw f32 bits (four independent chains of three-input max)
+__device__ __forceinline__ float rowmax64(const uint32_t (&v)[64]) {
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < 64; c += 8)
+#pragma unroll
+    for (int u = 0; u < 4; ++u) m[u] = max3(m[u], __uint_as_float(v[c + 2 * u]), __uint_as_float(v[c + 2 * u + 1]));
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
 // every (row, key) of a rows x keys tile is inside [0, Sk) and the band
 __device__ __forceinline__ bool tile_visible(int r0, int nr, int k0, int nk, int Sk, int window) {
   if (k0 + nk > Sk) return false;
@@ -120,18 +132,21 @@ __device__ __forceinline__ bool tile_visible(int r0, int nr, int k0, int nk, int
   return max(r0 + nr - 1 - k0, k0 + nk - 1 - r0) <= window;
 }
 
-// K-major [rows][64] bf16 tile (128-byte rows, 128B swizzle): descriptor at k-step kk (16 wide)
-__device__ __forceinline__ uint64_t kdesc(uint32_t base, int kk) { return make_sdesc(base + kk * 32, 16, 1024); }
-// the same tile read MN-major (its rows are the reduction index): 16 rows per k-step
-__device__ __forceinline__ uint64_t mndesc(uint32_t base, int kk) { return make_sdesc(base + kk * 2048, 8192, 1024); }
+// K-major [rows][64] bf16 tile (128-byte rows, 128B swizzle): descriptor of the tile, and the
+// descriptor at k-step kk (16 wide = 32 bytes further: +2 in the start-address field)
+__device__ __forceinline__ uint64_t kdesc0(uint32_t base) { return make_sdesc(base, 16, 1024); }
+__device__ __forceinline__ uint64_t kstep(uint64_t d0, int kk) { return d0 + (uint64_t)(2 * kk); }
+// the same tile read MN-major (its rows are the reduction index): 16 rows = 2048 bytes per k-step
+__device__ __forceinline__ uint64_t mndesc0(uint32_t base) { return make_sdesc(base, 8192, 1024); }
+__device__ __forceinline__ uint64_t mnstep(uint64_t d0, int kk) { return d0 + (uint64_t)(128 * kk); }
 
 struct Waiter {
   volatile int* abort_flag;
   int* err;
   __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity, int code) const {
-    if (*abort_flag) return false;
     const uint32_t a = smem_u32(bar);
-    if (mbar_try_wait(a, parity)) return true;
+    if (mbar_try_wait(a, parity)) return true;     // fast path: already complete
+    if (*abort_flag) return false;
     const unsigned long long t0 = globaltimer();
     for (uint32_t i = 1;; ++i) {
       if (mbar_try_wait(a, parity)) return true;
@@ -140,6 +155,33 @@ struct Waiter {
         if (globaltimer() - t0 > kWaitLimitNs) {
           record_error(err, code);
           *abort_flag = 1;
+          return false;
+        }
+      }
+    }
+  }
+};
+
+// Warp-wide bounded wait: every lane of the warp calls it and all get the same answer (the
+// warp stays converged for the .aligned tcgen05 instructions that follow).
+struct WaiterW {
+  volatile int* abort_flag;
+  int* err;
+  __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity, int code) const {
+    const uint32_t a = smem_u32(bar);
+    if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;   // fast path: already complete
+    if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 0;; ++i) {
+      if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
+      if ((i & 63u) == 63u) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitLimitNs)) {
+          if ((threadIdx.x & 31) == 0) {
+            record_error(err, code);
+            *abort_flag = 1;
+          }
+          __syncwarp();
           return false;
         }
       }
@@ -179,8 +221,9 @@ constexpr int NSTAGE = 4;
 
 // ============================================================================== forward
 // CTA: two 128-query tiles of one (b, h) (warpgroup g: rows qbase + 128 g ..), key tiles of 64.
-// TMEM, per warpgroup at 192 g: S0 [0, 64), S1 [64, 128) (double-buffered scores; P overwrites
-// the first 32 columns as packed bf16), O [128, 192).
+// TMEM, per warpgroup at 256 g: S0, S1, S2 at [0, 64), [64, 128), [128, 192) (scores of three
+// key tiles in flight; P overwrites the first 32 columns of its buffer as packed bf16), O at
+// [192, 256).
 // smem: Q0 16 KB | Q1 16 KB | 4 x (K 8 KB, V 8 KB) | barriers
 constexpr int F_SMEM = 32768 + NSTAGE * 16384 + 512;
 
@@ -195,8 +238,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + NSTAGE;
-  uint64_t* s_full = kv_empty + NSTAGE;   // [2 groups][2 buffers]
-  uint64_t* p_full = s_full + 4;          // [2]
+  uint64_t* s_full = kv_empty + NSTAGE;   // [2 groups][3 buffers]
+  uint64_t* p_full = s_full + 6;          // [2]
   uint64_t* o_done = p_full + 2;          // [2]
   uint64_t* o_full = o_done + 2;          // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
@@ -216,7 +259,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
+    for (int i = 0; i < 6; ++i) mbar_init(&s_full[i], 1);
     for (int g = 0; g < 2; ++g) {
       mbar_init(&p_full[g], 4);
       mbar_init(&o_done[g], 1);
@@ -236,7 +279,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const Waiter wait{abort_flag, a.err};
+  const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
+  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -253,42 +297,42 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {   // the whole warp walks the schedule (uniform operands); one elected lane issues
       const uint32_t id_qk = make_idesc_bf16(128, 64, 0, 0);   // S[128 q][64 k] = Q K^T
       const uint32_t id_pv = make_idesc_bf16(128, 64, 0, 1);   // O[128 q][64 d] += P V (V MN-major)
-      bool ok = wait(q_full, 0, kErrTimeoutFull);
+      bool ok = waitw(q_full, 0, kErrTimeoutFull);
       auto qk = [&](int j) -> bool {
         const int s = j % NSTAGE;
-        if (!wait(&kv_full[s], (uint32_t)(j / NSTAGE) & 1u, kErrTimeoutFull)) return false;
+        if (!waitw(&kv_full[s], (uint32_t)(j / NSTAGE) & 1u, kErrTimeoutFull)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sKV + s * 16384);
+        const uint64_t kd = kdesc0(smem_u32(sKV + s * 16384));
         for (int g = 0; g < ngrp; ++g) {
-          const uint32_t qa = smem_u32(sQ + 16384 * g), tS = tbase + 192 * g + 64 * (j & 1);
+          const uint64_t qd = kdesc0(smem_u32(sQ + 16384 * g));
+          const uint32_t tS = tbase + 256 * g + 64 * (j % 3);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16(tS, kdesc(qa, kk), kdesc(ka, kk), id_qk, kk > 0 ? 1u : 0u);
-          umma_commit(&s_full[2 * g + (j & 1)]);
+          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_qk, kk > 0 ? 1u : 0u);
+          umma_commit_w(&s_full[3 * g + (j % 3)]);
         }
         return true;
       };
-      if (ok && nkt > 0) ok = qk(0);
-      if (ok && nkt > 1) ok = qk(1);
+      for (int j = 0; j < 3 && j < nkt && ok; ++j) ok = qk(j);
       for (int j = 0; j < nkt && ok; ++j) {
         const int s = j % NSTAGE;
-        const uint32_t va = smem_u32(sKV + s * 16384) + 8192;
+        const uint64_t vd = mndesc0(smem_u32(sKV + s * 16384) + 8192);
         for (int g = 0; g < ngrp && ok; ++g) {
-          if (!wait(&p_full[g], (uint32_t)(j & 1), kErrTimeoutReady)) { ok = false; break; }
+          if (!waitw(&p_full[g], (uint32_t)(j & 1), kErrTimeoutReady)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t tS = tbase + 192 * g + 64 * (j & 1), tO = tbase + 192 * g + 128;
+          const uint32_t tS = tbase + 256 * g + 64 * (j % 3), tO = tbase + 256 * g + 192;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)   // 64 keys = 4 k-steps; P at S columns [0, 32)
-            umma_ts(tO, tS + kk * 8, mndesc(va, kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          umma_commit(&o_done[g]);
+            umma_ts_w(tO, tS + kk * 8, mnstep(vd, kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_commit_w(&o_done[g]);
         }
         if (!ok) break;
-        umma_commit(&kv_empty[s]);
-        if (j + 2 < nkt) ok = qk(j + 2);
+        umma_commit_w(&kv_empty[s]);
+        if (j + 3 < nkt) ok = qk(j + 3);
       }
-      for (int g = 0; g < ngrp; ++g) umma_commit(&o_full[g]);
+      for (int g = 0; g < ngrp; ++g) umma_commit_w(&o_full[g]);
     }
   } else {
     // ------------------------------------------------------------ softmax + epilogue
@@ -297,14 +341,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const int row = 32 * quarter + lane;
     const int r0 = qbase + 128 * g, qi = r0 + row;
     const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
-    const uint32_t tO = tbase + 192 * g + 128;
+    const uint32_t tO = tbase + 256 * g + 192;
     if (g < ngrp) {
       float m_used = -INFINITY, l = 0.f;
       bool ok = true;
       for (int j = 0; j < nkt; ++j) {
-        if (!wait(&s_full[2 * g + (j & 1)], (uint32_t)((j >> 1) & 1), kErrTimeoutAccum)) { ok = false; break; }
+        if (!waitw(&s_full[3 * g + (j % 3)], (uint32_t)((j / 3) & 1), kErrTimeoutAccum)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t tS = tbase + 192 * g + 64 * (j & 1);
+        const uint32_t tS = tbase + 256 * g + 64 * (j % 3);
         uint32_t v[64];
         tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
@@ -315,10 +359,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           for (int c = 0; c < 64; ++c)
             if (!visible(qi, k0 + c, a.Sk, a.window)) v[c] = __float_as_uint(-INFINITY);
         }
-        float mraw = -INFINITY;   // row max of the raw scores (scale > 0 keeps the order)
-#pragma unroll
-        for (int c = 0; c < 64; c += 2) mraw = fmaxf(mraw, fmaxf(__uint_as_float(v[c]), __uint_as_float(v[c + 1])));
-        const float mx = mraw * a.sl2;
+        const float mx = rowmax64(v) * a.sl2;   // (scale > 0 keeps the order of the raw scores)
         // lazy rescaling: keep the exponent base unless the row max grew by more than 2^8
         const bool grow = mx > m_used + 8.f;
         float alpha = 1.f;
@@ -326,9 +367,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mx);
           m_used = mx;
         }
-        // O is stable once the previous tile's P V has completed
-        if (j > 0 && !wait(&o_done[g], (uint32_t)((j - 1) & 1), kErrTimeoutAccum)) { ok = false; break; }
+        // O is stable once the previous tile's P V has completed (o_done phase j - 1).  That phase
+        // is consumed exactly once per tile: here when O must be rescaled, else just before P_j is
+        // handed to the MMA (it has normally completed long before).
+        bool waited = false;
         if (__any_sync(0xffffffffu, grow && j > 0)) {
+          if (!waitw(&o_done[g], (uint32_t)((j - 1) & 1), kErrTimeoutAccum)) { ok = false; break; }
+          waited = true;
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[16];
@@ -342,7 +387,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         l *= alpha;
         const float mb = m_used == -INFINITY ? 0.f : m_used;
         const uint64_t sc2 = f2(a.sl2, a.sl2), nb2 = f2(-mb, -mb);
-        uint64_t lsum = f2(0.f, 0.f);
+        uint64_t lsum[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           uint32_t pk[16];
@@ -352,22 +397,24 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             f2split(ffma2(f2(__uint_as_float(v[32 * c + 2 * e]), __uint_as_float(v[32 * c + 2 * e + 1])), sc2, nb2),
                     x0, x1);
             const float p0 = ex2(x0), p1 = ex2(x1);
-            lsum = fadd2(lsum, f2(p0, p1));
+            lsum[e & 1] = fadd2(lsum[e & 1], f2(p0, p1));
             pk[e] = pack_bf16x2(p0, p1);
           }
           tmem_st16(tS + lane_off + 16 * c, pk);
         }
         {
-          float l0, l1;
-          f2split(lsum, l0, l1);
-          l += l0 + l1;
+          float l0, l1, l2, l3;
+          f2split(lsum[0], l0, l1);
+          f2split(lsum[1], l2, l3);
+          l += (l0 + l1) + (l2 + l3);
         }
         tmem_st_wait();
         tc_fence_before();
+        if (j > 0 && !waited && !waitw(&o_done[g], (uint32_t)((j - 1) & 1), kErrTimeoutAccum)) { ok = false; break; }
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[g]);
       }
-      const bool have = ok && wait(&o_full[g], 0, kErrTimeoutAccum) && nkt > 0;
+      const bool have = ok && waitw(&o_full[g], 0, kErrTimeoutAccum) && nkt > 0;
       tc_fence_after();
       if (ok && nkt == 0 && qi < a.Sq) {     // no visible key: O = 0 (an empty softmax row)
         uint4* dst = reinterpret_cast<uint4*>(a.o + b * a.o_sb + h * a.o_sh + (long)qi * a.o_ld);
@@ -405,52 +452,85 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // ============================================================================== dq pass
-// CTA: 128 queries of one (b, h); key tiles of 64, warpgroup g takes tiles j = g, g + 2, ...
-// TMEM: buffer g at 128 g: S [0, 64) (dS overwrites [0, 32) as packed bf16), dP [64, 128);
-// dQ at 256 (64 columns).  The softmax threads also form D = rowsum(dO o O) for their row
-// (written to Dsum for the dk / dv pass).
-// smem: Q 16 KB | dO 16 KB | 4 x (K 8 KB, V 8 KB) | barriers
-constexpr int Q_SMEM = 32768 + NSTAGE * 16384 + 512;
+// Persistent: CTA c walks the work items c, c + gridDim.x, ...; an item is 128 queries of one
+// (b, h) (items of one (b, h) are adjacent, so co-running CTAs share its K / V in L2).  The key
+// tiles (64) of consecutive items form one stream: the TMA ring, the three score buffers and the
+// warpgroup that handles a tile (the stream index's parity) all run on across items, and the
+// next item's Q / dO load while the current item finishes.
+// TMEM: score buffers at 128 b (b < 3): S [0, 64) (dS overwrites [0, 32) as packed bf16),
+// dP [64, 128); two dQ accumulators at 384 and 448 (alternate items).  The softmax threads also
+// form D = rowsum(dO o O) of their row (stored to Dsum for the dk / dv pass).
+// The row's O comes in with Q and dO (TMA, an item ahead), so D needs no global load at the
+// item boundary; dQ leaves through swizzled shared-memory staging and TMA stores.
+// smem: 2 x (Q 16 KB, dO 16 KB, O 16 KB) | 5 x (K 8 KB, V 8 KB) | 8 x 4 KB dQ staging | barriers
+constexpr int Q_STAGES = 5;
+constexpr int Q_SMEM = 98304 + Q_STAGES * 16384 + 32768 + 512;
+
+struct ItemCursor {   // walks this CTA's items and their key tiles
+  int item, nitems, step, qtiles, Sq, Sk, window, tile;
+  int bh, r0, t0, t1;       // current item: (b, h), first row, visible other-side tile range
+  __device__ __forceinline__ void load() {
+    bh = item / qtiles;
+    r0 = (item % qtiles) * 128;
+    tile_range(r0, 128, Sk, window, tile, t0, t1);
+  }
+  __device__ __forceinline__ bool valid() const { return item < nitems; }
+  __device__ __forceinline__ void next() {
+    item += step;
+    if (item < nitems) load();
+  }
+};
 
 __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                       const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                      const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_dq,
                       const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sdO = smem + 16384;
-  uint8_t* sKV = smem + 32768;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 32768 + NSTAGE * 16384);
-  uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;
-  uint64_t* kv_empty = kv_full + NSTAGE;
-  uint64_t* s_full = kv_empty + NSTAGE;   // [2]
-  uint64_t* ds_full = s_full + 2;         // [2]
-  uint64_t* acc_full = ds_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint8_t* sQd = smem;                  // [2 items][Q 16 KB | dO 16 KB | O 16 KB]
+  uint8_t* sKV = smem + 98304;
+  uint8_t* sStage = sKV + Q_STAGES * 16384;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sStage + 32768);
+  uint64_t* q_full = bars;              // [2]
+  uint64_t* q_empty = q_full + 2;       // [2]
+  uint64_t* kv_full = q_empty + 2;      // [Q_STAGES]
+  uint64_t* kv_empty = kv_full + Q_STAGES;
+  uint64_t* s_full = kv_empty + Q_STAGES;   // [3 buffers]
+  uint64_t* ds_full = s_full + 3;         // [3 buffers]
+  uint64_t* acc_full = ds_full + 3;       // [2]
+  uint64_t* acc_empty = acc_full + 2;     // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int q0 = blockIdx.x * 128;
-  int kt0, kt1;
-  tile_range(q0, 128, a.Sk, a.window, 64, kt0, kt1);
-  const int nkt = kt1 - kt0;
+  const int qtiles = (a.Sq + 127) / 128;
+  const int nitems = a.B * a.H * qtiles;
+  auto cursor = [&]() {
+    ItemCursor c{(int)blockIdx.x, nitems, (int)gridDim.x, qtiles, a.Sq, a.Sk, a.window, 64, 0, 0, 0, 0};
+    if (c.valid()) c.load();
+    return c;
+  };
 
   if (warp == 0 && lane == 0) {
-    mbar_init(q_full, 1);
-    for (int s = 0; s < NSTAGE; ++s) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);
+    }
+    for (int s = 0; s < Q_STAGES; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(&s_full[g], 1);
-      mbar_init(&ds_full[g], 4);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 4);
     }
-    mbar_init(acc_full, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
     tma_prefetch_desc(&tm_k);
     tma_prefetch_desc(&tm_v);
   }
@@ -462,137 +542,232 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tQ = tbase + 256;
-  const Waiter wait{abort_flag, a.err};
+  const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
+  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 32768);
-      load_rows(sQ, &tm_q, q_full, a.q_tm, b, h, q0);
-      load_rows(sdO, &tm_do, q_full, a.do_tm, b, h, q0);
-      for (int j = 0; j < nkt; ++j) {
-        const int s = j % NSTAGE;
-        const uint32_t use = (uint32_t)(j / NSTAGE);
-        if (j >= NSTAGE && !wait(&kv_empty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) break;
-        uint8_t* st = sKV + s * 16384;
-        mbar_arrive_expect_tx(&kv_full[s], 16384);
-        load_rows(st, &tm_k, &kv_full[s], a.k_tm, b, h, (kt0 + j) * 64);
-        load_rows(st + 8192, &tm_v, &kv_full[s], a.v_tm, b, h, (kt0 + j) * 64);
+      ItemCursor c = cursor();
+      int t = 0, ii = 0;     // ii counts the items that have key tiles (empty ones touch no barrier)
+      bool ok = true;
+      for (; c.valid() && ok; c.next()) {
+        if (c.t0 == c.t1) continue;
+        const int ib = ii & 1;
+        const int b = c.bh / a.H, h = c.bh % a.H;
+        if (ii >= 2 && !wait(&q_empty[ib], (uint32_t)(((ii >> 1) - 1) & 1), kErrTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&q_full[ib], 49152);
+        load_rows(sQd + 49152 * ib, &tm_q, &q_full[ib], a.q_tm, b, h, c.r0);
+        load_rows(sQd + 49152 * ib + 16384, &tm_do, &q_full[ib], a.do_tm, b, h, c.r0);
+        load_rows(sQd + 49152 * ib + 32768, &tm_o, &q_full[ib], a.o_tm, b, h, c.r0);
+        for (int kt = c.t0; kt < c.t1; ++kt, ++t) {
+          const int s = t % Q_STAGES;
+          const uint32_t use = (uint32_t)(t / Q_STAGES);
+          if (t >= Q_STAGES && !wait(&kv_empty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) { ok = false; break; }
+          uint8_t* st = sKV + s * 16384;
+          mbar_arrive_expect_tx(&kv_full[s], 16384);
+          load_rows(st, &tm_k, &kv_full[s], a.k_tm, b, h, kt * 64);
+          load_rows(st + 8192, &tm_v, &kv_full[s], a.v_tm, b, h, kt * 64);
+        }
+        ++ii;
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {   // the whole warp walks the schedule (uniform operands); one elected lane issues
       const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S = Q K^T, dP = dO V^T  [128 q][64 k]
       const uint32_t id_dq = make_idesc_bf16(128, 64, 0, 1);   // dQ[128 q][64 d] += dS K (K MN-major)
-      bool ok = wait(q_full, 0, kErrTimeoutFull);
-      const uint32_t qa = smem_u32(sQ), da = smem_u32(sdO);
-      auto sd = [&](int j) -> bool {
-        const int s = j % NSTAGE;
-        if (!wait(&kv_full[s], (uint32_t)(j / NSTAGE) & 1u, kErrTimeoutFull)) return false;
+      bool ok = true;
+      // score cursor (runs up to three tiles ahead) and dQ cursor over the same tile stream; each
+      // rests on a key tile of an item that has some (the item counter ii, which picks the Q / dO
+      // buffer and the accumulator, counts only those items)
+      auto normalize = [&](ItemCursor& c, int& kt) {
+        while (c.valid() && c.t0 == c.t1) { c.next(); if (c.valid()) kt = c.t0; }
+      };
+      auto advance = [&](ItemCursor& c, int& ii, int& kt) {
+        if (++kt < c.t1) return;
+        c.next();
+        ++ii;
+        if (c.valid()) kt = c.t0;
+        normalize(c, kt);
+      };
+      ItemCursor cs = cursor(), cd = cursor();
+      int ii_s = 0, kt_s = cs.valid() ? cs.t0 : 0, t_s = 0;
+      int ii_d = 0, kt_d = cd.valid() ? cd.t0 : 0, t_d = 0;
+      normalize(cs, kt_s);
+      normalize(cd, kt_d);
+      auto issue_sd = [&]() -> bool {
+        if (!cs.valid()) return true;
+        const int ib = ii_s & 1;
+        if (kt_s == cs.t0 && !waitw(&q_full[ib], (uint32_t)((ii_s >> 1) & 1), kErrTimeoutFull)) return false;
+        const int s = t_s % Q_STAGES;
+        if (!waitw(&kv_full[s], (uint32_t)(t_s / Q_STAGES) & 1u, kErrTimeoutFull)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(sKV + s * 16384), va = ka + 8192, tS = tbase + 128 * (j & 1);
+        const uint32_t qa = smem_u32(sQd + 49152 * ib);
+        const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 16384);
+        const uint32_t ka = smem_u32(sKV + s * 16384), tS = tbase + 128 * (t_s % 3);
+        const uint64_t kd = kdesc0(ka), vd = kdesc0(ka + 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tS, kdesc(qa, kk), kdesc(ka, kk), id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tS + 64, kdesc(da, kk), kdesc(va, kk), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[j & 1]);
+        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
+        umma_commit_w(&s_full[t_s % 3]);
+        ++t_s;
+        advance(cs, ii_s, kt_s);
         return true;
       };
-      if (ok && nkt > 0) ok = sd(0);
-      if (ok && nkt > 1) ok = sd(1);
-      for (int j = 0; j < nkt && ok; ++j) {
-        const int s = j % NSTAGE;
-        if (!wait(&ds_full[j & 1], (uint32_t)((j >> 1) & 1), kErrTimeoutReady)) { ok = false; break; }
+      for (int i = 0; i < 3 && ok; ++i) ok = issue_sd();
+      while (ok) {
+        if (!cd.valid()) break;
+        const int ia = ii_d & 1;
+        const bool first = kt_d == cd.t0, last = kt_d + 1 == cd.t1;
+        if (!waitw(&ds_full[t_d % 3], (uint32_t)((t_d / 3) & 1), kErrTimeoutReady)) { ok = false; break; }
+        if (first && ii_d >= 2 && !waitw(&acc_empty[ia], (uint32_t)(((ii_d >> 1) - 1) & 1), kErrTimeoutOther)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
-        const uint32_t ka = smem_u32(sKV + s * 16384), tS = tbase + 128 * (j & 1);
+        const int s = t_d % Q_STAGES;
+        const uint64_t kmn = mndesc0(smem_u32(sKV + s * 16384));
+        const uint32_t tS = tbase + 128 * (t_d % 3), tQ = tbase + 384 + 64 * ia;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)   // 64 keys = 4 k-steps; dS at S columns [0, 32)
-          umma_ts(tQ, tS + kk * 8, mndesc(ka, kk), id_dq, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&kv_empty[s]);
-        if (j + 2 < nkt) ok = sd(j + 2);
+          umma_ts_w(tQ, tS + kk * 8, mnstep(kmn, kk), id_dq, (!first || kk > 0) ? 1u : 0u);
+        umma_commit_w(&kv_empty[s]);
+        if (last) {
+          umma_commit_w(&acc_full[ia]);
+          umma_commit_w(&q_empty[ii_d & 1]);
+        }
+        ++t_d;
+        advance(cd, ii_d, kt_d);
+        ok = issue_sd();
       }
-      umma_commit(acc_full);
     }
   } else {
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = 32 * quarter + lane;
-    const int qi = q0 + row;
     const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
-    const bool qok = qi < a.Sq;
-    const float lse = qok ? a.lse_in[(long)bh * a.Sq + qi] : INFINITY;
-    bool ok = wait(q_full, 0, kErrTimeoutFull);
-    // D = rowsum(dO o O): dO from the swizzled smem tile, O from global
-    float Dq = 0.f;
-    if (ok && qok) {
-      const uint4* orow = reinterpret_cast<const uint4*>(a.o + b * a.o_sb + h * a.o_sh + (long)qi * a.o_ld);
+    ItemCursor c = cursor();
+    bool ok = true;
+    int t = 0, ii = 0;
+    uint8_t* stg = sStage + (warp - 2) * 4096;   // this warp's 32 rows x 32 f32 of dQ
+    // lse of the row in the next item that has key tiles, fetched one item ahead
+    auto next_item = [&](ItemCursor cn) {
+      cn.next();
+      while (cn.valid() && cn.t0 == cn.t1) cn.next();
+      return cn;
+    };
+    auto fetch_lse = [&](const ItemCursor& cn) -> float {
+      if (!cn.valid()) return INFINITY;
+      const int qi = cn.r0 + row;
+      return qi < a.Sq ? a.lse_in[(long)cn.bh * a.Sq + qi] : INFINITY;
+    };
+    ItemCursor cf = c;
+    while (cf.valid() && cf.t0 == cf.t1) cf.next();
+    float lse_next = fetch_lse(cf);
+    for (; c.valid(); c.next()) {
+      const int ib = ii & 1, ia = ii & 1;
+      const int b = c.bh / a.H, h = c.bh % a.H;
+      const int q0 = c.r0, qi = q0 + row;
+      const bool qok = qi < a.Sq;
+      const int nkt = c.t1 - c.t0;
+      if (nkt == 0) {     // no visible key: dQ = 0; the item touches no barrier or buffer
+        if (qok) {
+          float4* dz = reinterpret_cast<float4*>(a.dq + b * a.dq_sb + h * a.dq_sh + (long)qi * a.dq_ld + 32 * g);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 ov = orow[c];
-        const uint4 dv = *reinterpret_cast<const uint4*>(sdO + row * 128 + ((c ^ (row & 7)) << 4));
-        const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
-        const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+          for (int cc = 0; cc < 8; ++cc) dz[cc] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (g == 0) a.Dsum[(long)c.bh * a.Sq + qi] = 0.f;
+        }
+        continue;
+      }
+      ++ii;
+      const float lse = lse_next;
+      lse_next = fetch_lse(next_item(c));
+      if (ok) ok = waitw(&q_full[ib], (uint32_t)(((ii - 1) >> 1) & 1), kErrTimeoutFull);
+      // D = rowsum(dO o O) from the swizzled dO and O tiles in shared memory
+      float Dq = 0.f;
+      if (ok) {
+        const uint8_t* sdO = sQd + 49152 * ib + 16384;
+        const uint8_t* sO = sdO + 16384;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 of = __bfloat1622float2(o2[e]), df = __bfloat1622float2(d2[e]);
-          Dq = fmaf(of.x, df.x, Dq);
-          Dq = fmaf(of.y, df.y, Dq);
+        for (int cc = 0; cc < 8; ++cc) {
+          const int off = row * 128 + ((cc ^ (row & 7)) << 4);
+          const uint4 ov = *reinterpret_cast<const uint4*>(sO + off);
+          const uint4 dv = *reinterpret_cast<const uint4*>(sdO + off);
+          const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
+          const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 of = __bfloat1622float2(o2[e]), df = __bfloat1622float2(d2[e]);
+            Dq = fmaf(of.x, df.x, Dq);
+            Dq = fmaf(of.y, df.y, Dq);
+          }
+        }
+        if (!qok) Dq = 0.f;
+        if (g == 0 && qok) a.Dsum[(long)c.bh * a.Sq + qi] = Dq;
+      }
+      for (int j = 0; j < nkt; ++j, ++t) {
+        if ((t & 1) != g || !ok) continue;
+        if (!waitw(&s_full[t % 3], (uint32_t)((t / 3) & 1), kErrTimeoutAccum)) { ok = false; continue; }
+        tc_fence_after();
+        const uint32_t tS = tbase + 128 * (t % 3);
+        uint32_t sv[64], pv[64];
+        tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
+        tmem_ld32(tS + 64 + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
+        tmem_ld_wait();
+        const int k0 = (c.t0 + j) * 64;
+        if (!tile_visible(q0, 128, k0, 64, a.Sk, a.window)) {
+#pragma unroll
+          for (int cc = 0; cc < 64; ++cc)
+            if (!visible(qi, k0 + cc, a.Sk, a.window)) sv[cc] = __float_as_uint(-INFINITY);
+        }
+        const uint64_t sc2 = f2(a.sl2, a.sl2), nl2 = f2(-lse, -lse), nd2 = f2(-Dq, -Dq);
+        uint32_t pk[32];   // dS row as packed bf16 pairs: column e holds keys 2e, 2e + 1
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float x0, x1, d0, d1;
+          f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
+          const uint64_t pp = f2(ex2(x0), ex2(x1));
+          f2split(fmul2(pp, fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0, d1);
+          pk[e] = pack_bf16x2(d0, d1);
+        }
+        tmem_st16(tS + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
+        tmem_st16(tS + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ds_full[t % 3]);
+      }
+      // epilogue of the item: warpgroup g stores dQ columns [32 g, 32 g + 32) of its 32 rows
+      const bool have = ok && waitw(&acc_full[ia], (uint32_t)(((ii - 1) >> 1) & 1), kErrTimeoutAccum);
+      ok = have;
+      tc_fence_after();
+      if (have) {
+        uint32_t o[32];
+        tmem_ld32(tbase + 384 + 64 * ia + 32 * g + lane_off, o);
+        tmem_ld_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[ia]);   // the accumulator is free again
+        if (lane == 0) bulk_wait_read<0>();             // the previous item's store has read stg
+        __syncwarp();
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc)
+          *reinterpret_cast<float4*>(stg + lane * 128 + ((cc ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(o[4 * cc]) * a.scale, __uint_as_float(o[4 * cc + 1]) * a.scale,
+                          __uint_as_float(o[4 * cc + 2]) * a.scale, __uint_as_float(o[4 * cc + 3]) * a.scale);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const int r0 = q0 + 32 * quarter;
+          if (a.dq_tm) tma_store_4d(&tm_dq, stg, 32 * g, h, r0, b);
+          else tma_store_4d(&tm_dq, stg, 32 * g, r0, h, b);
+          bulk_commit();
         }
       }
-      if (g == 0) a.Dsum[(long)bh * a.Sq + qi] = Dq;
     }
-    for (int j = g; j < nkt && ok; j += 2) {
-      if (!wait(&s_full[g], (uint32_t)((j >> 1) & 1), kErrTimeoutAccum)) { ok = false; break; }
-      tc_fence_after();
-      const uint32_t tS = tbase + 128 * g;
-      uint32_t sv[64], pv[64];
-      tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
-      tmem_ld32(tS + 64 + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
-      tmem_ld_wait();
-      const int k0 = (kt0 + j) * 64;
-      if (!tile_visible(q0, 128, k0, 64, a.Sk, a.window)) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (!visible(qi, k0 + c, a.Sk, a.window)) sv[c] = __float_as_uint(-INFINITY);
-      }
-      const uint64_t sc2 = f2(a.sl2, a.sl2), nl2 = f2(-lse, -lse), nd2 = f2(-Dq, -Dq);
-      uint32_t pk[32];   // dS row as packed bf16 pairs: column e holds keys 2e, 2e + 1
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        float x0, x1, d0, d1;
-        f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
-        const uint64_t pp = f2(ex2(x0), ex2(x1));
-        f2split(fmul2(pp, fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0, d1);
-        pk[e] = pack_bf16x2(d0, d1);
-      }
-      tmem_st16(tS + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-      tmem_st16(tS + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ds_full[g]);
-    }
-    const bool have = ok && wait(acc_full, 0, kErrTimeoutAccum) && nkt > 0;
-    tc_fence_after();
-    // warpgroup g writes dQ columns [32 g, 32 g + 32)
-    float4* dst = reinterpret_cast<float4*>(a.dq + b * a.dq_sb + h * a.dq_sh + (long)qi * a.dq_ld + 32 * g);
-    if (ok && nkt == 0 && qok) {
-#pragma unroll
-      for (int c = 0; c < 8; ++c) dst[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    if (have) {
-      uint32_t o[32];
-      tmem_ld32(tQ + lane_off + 32 * g, o);
-      tmem_ld_wait();
-      if (qok) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          dst[c] = make_float4(__uint_as_float(o[4 * c]) * a.scale, __uint_as_float(o[4 * c + 1]) * a.scale,
-                               __uint_as_float(o[4 * c + 2]) * a.scale, __uint_as_float(o[4 * c + 3]) * a.scale);
-      }
-    }
+    if (lane == 0) bulk_wait_all();
   }
   __syncthreads();
   if (warp == 1) {
@@ -603,8 +778,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
 // ============================================================================== dkdv pass
 // CTA: 128 keys of one (b, h); query tiles of 64, warpgroup g takes tiles i = g, g + 2, ...
-// TMEM: buffer g at 128 g: S^T [0, 64) (P^T overwrites [0, 32)), dP^T [64, 128) (dS^T overwrites
-// [64, 96)); dV at 256, dK at 320.
+// TMEM: three buffers (query tiles in flight) at 128 b: S^T [0, 64) (P^T overwrites [0, 32)),
+// dP^T [64, 128) (dS^T overwrites [64, 96)); dV at 384, dK at 448.
 // smem: K 16 KB | V 16 KB | 4 x (Q 8 KB, dO 8 KB) | lse / D per warpgroup (x2) | barriers
 constexpr int KV_SMEM = 32768 + NSTAGE * 16384 + 2048 + 512;
 
@@ -622,9 +797,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
   uint64_t* q_empty = q_full + NSTAGE;
-  uint64_t* s_full = q_empty + NSTAGE;    // [2]
-  uint64_t* ds_full = s_full + 2;         // [2]
-  uint64_t* acc_full = ds_full + 2;
+  uint64_t* s_full = q_empty + NSTAGE;    // [3 buffers]
+  uint64_t* ds_full = s_full + 3;         // [3 buffers]
+  uint64_t* acc_full = ds_full + 3;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -641,9 +816,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&q_full[s], 1);
       mbar_init(&q_empty[s], 1);
     }
-    for (int g = 0; g < 2; ++g) {
-      mbar_init(&s_full[g], 1);
-      mbar_init(&ds_full[g], 4);
+    for (int i = 0; i < 3; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&ds_full[i], 4);
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -659,8 +834,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tV = tbase + 256, tK = tbase + 320;
-  const Waiter wait{abort_flag, a.err};
+  const uint32_t tV = tbase + 384, tK = tbase + 448;
+  const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
+  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -678,40 +854,41 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    {   // the whole warp walks the schedule (uniform operands); one elected lane issues
       const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S^T = K Q^T, dP^T = V dO^T  [128 k][64 q]
       const uint32_t id_g = make_idesc_bf16(128, 64, 0, 1);    // dV / dK [128 k][64 d] (dO / Q MN-major)
-      bool ok = wait(kv_full, 0, kErrTimeoutFull);
-      const uint32_t ka = smem_u32(sK), va = smem_u32(sV);
+      bool ok = waitw(kv_full, 0, kErrTimeoutFull);
+      const uint64_t kd = kdesc0(smem_u32(sK)), vd = kdesc0(smem_u32(sV));
       auto sd = [&](int i) -> bool {
         const int s = i % NSTAGE;
-        if (!wait(&q_full[s], (uint32_t)(i / NSTAGE) & 1u, kErrTimeoutFull)) return false;
+        if (!waitw(&q_full[s], (uint32_t)(i / NSTAGE) & 1u, kErrTimeoutFull)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sQd + s * 16384), da = qa + 8192, tS = tbase + 128 * (i & 1);
+        const uint32_t qa = smem_u32(sQd + s * 16384), tS = tbase + 128 * (i % 3);
+        const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tS, kdesc(ka, kk), kdesc(qa, kk), id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(kd, kk), kstep(qd, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16(tS + 64, kdesc(va, kk), kdesc(da, kk), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(&s_full[i & 1]);
+        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(vd, kk), kstep(dd, kk), id_s, kk > 0 ? 1u : 0u);
+        umma_commit_w(&s_full[i % 3]);
         return true;
       };
-      if (ok && nqt > 0) ok = sd(0);
-      if (ok && nqt > 1) ok = sd(1);
+      for (int i = 0; i < 3 && i < nqt && ok; ++i) ok = sd(i);
       for (int i = 0; i < nqt && ok; ++i) {
         const int s = i % NSTAGE;
-        if (!wait(&ds_full[i & 1], (uint32_t)((i >> 1) & 1), kErrTimeoutReady)) { ok = false; break; }
+        if (!waitw(&ds_full[i % 3], (uint32_t)((i / 3) & 1), kErrTimeoutReady)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t qa = smem_u32(sQd + s * 16384), da = qa + 8192, tS = tbase + 128 * (i & 1);
+        const uint32_t qa = smem_u32(sQd + s * 16384), tS = tbase + 128 * (i % 3);
+        const uint64_t qmn = mndesc0(qa), dmn = mndesc0(qa + 8192);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)   // 64 queries = 4 k-steps; P^T at S^T columns [0, 32)
-          umma_ts(tV, tS + kk * 8, mndesc(da, kk), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+          umma_ts_w(tV, tS + kk * 8, mnstep(dmn, kk), id_g, (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)   // dS^T at dP^T columns [0, 32)
-          umma_ts(tK, tS + 64 + kk * 8, mndesc(qa, kk), id_g, (i > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&q_empty[s]);
-        if (i + 2 < nqt) ok = sd(i + 2);
+          umma_ts_w(tK, tS + 64 + kk * 8, mnstep(qmn, kk), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_w(&q_empty[s]);
+        if (i + 3 < nqt) ok = sd(i + 3);
       }
-      umma_commit(acc_full);
+      umma_commit_w(acc_full);
     }
   } else {
     const int g = (warp - 2) >> 2;
@@ -722,22 +899,26 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
     bool ok = true;
     int it = 0;
+    // thread t holds lse (t < 64) or D (t >= 64) of query t % 64 of a tile; the value for the
+    // group's next tile is fetched one tile ahead so its latency hides behind the current one
+    auto fetch = [&](int i) -> float {
+      const int qi = (qt0 + i) * 64 + (t & 63);
+      if (qi >= a.Sq) return t < 64 ? INFINITY : 0.f;
+      return t < 64 ? a.lse_in[(long)bh * a.Sq + qi] : a.Dsum[(long)bh * a.Sq + qi];
+    };
+    float next = g < nqt ? fetch(g) : 0.f;
     for (int i = g; i < nqt; i += 2, ++it) {
       const int q0 = (qt0 + i) * 64;
       float* lse_b = s_ld + 256 * g + 128 * (it & 1);
       float* D_b = lse_b + 64;
-      {
-        const int c = t & 63, qi = q0 + c;
-        const bool qok = qi < a.Sq;
-        if (t < 64) lse_b[c] = qok ? a.lse_in[(long)bh * a.Sq + qi] : INFINITY;
-        else D_b[c] = qok ? a.Dsum[(long)bh * a.Sq + qi] : 0.f;
-      }
+      lse_b[t] = next;               // lse_b[64 + c] is D_b[c]
+      if (i + 2 < nqt) next = fetch(i + 2);
       if (g == 0) named_bar(1, 128);   // every warp of the group passes it once per tile, also after an abort
       else named_bar(2, 128);
-      if (ok) ok = wait(&s_full[g], (uint32_t)(it & 1), kErrTimeoutAccum);
+      if (ok) ok = waitw(&s_full[i % 3], (uint32_t)((i / 3) & 1), kErrTimeoutAccum);
       if (!ok) continue;
       tc_fence_after();
-      const uint32_t tS = tbase + 128 * g;
+      const uint32_t tS = tbase + 128 * (i % 3);
       uint32_t sv[64], pv[64];
       tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
       tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
@@ -772,9 +953,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&ds_full[g]);
+      if (lane == 0) mbar_arrive(&ds_full[i % 3]);
     }
-    const bool have = ok && wait(acc_full, 0, kErrTimeoutAccum) && nqt > 0;
+    const bool have = ok && waitw(acc_full, 0, kErrTimeoutAccum) && nqt > 0;
     tc_fence_after();
     const bool kok = kj < a.Sk;
     // warpgroup 0 writes dV, warpgroup 1 writes dK
@@ -807,14 +988,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }
 
 // ------------------------------------------------------------------------------ host side
-// 4-D tensor map over a strided (b, h, s, d) bf16 tensor: the smaller of the head / row strides
-// goes second so the strides grow; the box is `rows` rows x 64 d of one (b, h).
-int make_map4(CUtensorMap* m, const __nv_bfloat16* base, long sb, long sh, long ld, int B, int H, int S, int rows,
-              int& tm, std::string& err) {
+// 4-D tensor map over a strided (b, h, s, d) tensor with 64 values per row (d): the smaller of
+// the head / row strides goes second so the strides grow; the box is `rows` rows x `box_d`
+// values of one (b, h) (box_d x element size = 128 bytes, the swizzle span).
+int make_map4t(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* base, long sb, long sh, long ld,
+               int B, int H, int S, int box_d, int rows, int& tm, std::string& err) {
   PFN_encodeTiled enc = encode_tiled_fn(err);
   if (!enc) return 1;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (sh % 8) || (ld % 8) || (sb % 8)) {
-    err = "attention: tensor strides must be multiples of 8 elements";
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (sh * esize) % 16 || (ld * esize) % 16 || (sb * esize) % 16) {
+    err = "attention: tensor rows and strides must be 16-byte aligned";
     return 1;
   }
   tm = sh <= ld ? 1 : 0;
@@ -828,17 +1010,22 @@ int make_map4(CUtensorMap* m, const __nv_bfloat16* base, long sb, long sh, long 
     return 1;
   }
   cuuint64_t dims[4] = {64, (cuuint64_t)n1, (cuuint64_t)n2, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)s1 * 2, (cuuint64_t)s2 * 2, (cuuint64_t)s3 * 2};
-  cuuint32_t box[4] = {64, tm ? 1u : (cuuint32_t)rows, tm ? (cuuint32_t)rows : 1u, 1};
+  cuuint64_t strides[3] = {(cuuint64_t)(s1 * esize), (cuuint64_t)(s2 * esize), (cuuint64_t)(s3 * esize)};
+  cuuint32_t box[4] = {(cuuint32_t)box_d, tm ? 1u : (cuuint32_t)rows, tm ? (cuuint32_t)rows : 1u, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<__nv_bfloat16*>(base), dims, strides, box,
-                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     err = "attention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")";
     return 1;
   }
   return 0;
+}
+
+int make_map4(CUtensorMap* m, const __nv_bfloat16* base, long sb, long sh, long ld, int B, int H, int S, int rows,
+              int& tm, std::string& err) {
+  return make_map4t(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, sb, sh, ld, B, H, S, 64, rows, tm, err);
 }
 
 TcArgs tc_args(const AttnArgs& p) {
@@ -901,15 +1088,19 @@ int attn_tc_grads(Ctx* c, const AttnArgs& p, bool want_dkdv, std::string& err) {
   TcArgs a = tc_args(p);
   a.err = c->d_err;
   {
-    CUtensorMap mq, mdo, mk, mv;
+    CUtensorMap mq, mdo, mk, mv, mo, mdq;
     if (make_map4(&mq, p.q, p.q_sb, p.q_sh, p.q_ld, p.B, p.H, p.Sq, 128, a.q_tm, err) ||
         make_map4(&mdo, p.dO, p.dO_sb, p.dO_sh, p.dO_ld, p.B, p.H, p.Sq, 128, a.do_tm, err) ||
         make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, 64, a.k_tm, err) ||
-        make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 64, a.v_tm, err))
+        make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 64, a.v_tm, err) ||
+        make_map4(&mo, p.o, p.o_sb, p.o_sh, p.o_ld, p.B, p.H, p.Sq, 128, a.o_tm, err) ||
+        make_map4t(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.dq, p.dq_sb, p.dq_sh, p.dq_ld, p.B, p.H, p.Sq, 32, 32,
+                   a.dq_tm, err))
       return 1;
     ProfScope prof_(c, "attn.bwd_dq");
-    dim3 grid((unsigned)((p.Sq + 127) / 128), (unsigned)(p.B * p.H));
-    attn_tc_dq_kernel<<<grid, kThreadsTC, smem_req(Q_SMEM), c->stream>>>(mq, mdo, mk, mv, a);
+    const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);   // persistent: one CTA per SM at most
+    const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
+    attn_tc_dq_kernel<<<grid, kThreadsTC, smem_req(Q_SMEM), c->stream>>>(mq, mdo, mk, mv, mo, mdq, a);
     if (check_launch("attn tc dq", err)) return 1;
   }
   if (want_dkdv) {
