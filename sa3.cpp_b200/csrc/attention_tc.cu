@@ -205,13 +205,15 @@ __device__ __forceinline__ void tile_range(int r0, int n, int other, int window,
   }
 }
 
-// Warp roles of all three kernels (10 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA
-// issuer, warps 2-5 = warpgroup 0 and warps 6-9 = warpgroup 1 of softmax threads (thread <->
-// TMEM lane <-> tile row; warp w reaches lanes 32 (w % 4) .. +32).  Streamed tiles are 64 rows
+// Warp roles of all three kernels (11 warps): warp 0 TMA producer, warp 1 TMEM owner and issuer
+// of the score MMAs, warp 10 issuer of the gradient / output MMAs (two issue streams, synchronised
+// through barriers, so neither waits on the other's instruction issue), warps 2-5 = warpgroup 0
+// and warps 6-9 = warpgroup 1 of softmax threads (thread <-> TMEM lane <-> tile row; warp w
+// reaches lanes 32 (w % 4) .. +32).  Streamed tiles are 64 rows
 // and sit in a 4-deep ring.  The two warpgroups keep the tensor core busy while they work: in
 // the forward each owns its own 128-query tile; in the backward passes they take alternate
 // streamed tiles and the MMA thread folds their results into one accumulator in tile order.
-constexpr int kWarpsTC = 10;
+constexpr int kWarpsTC = 11;
 // Each CTA holds all 512 TMEM columns; a shared-memory request above half the SM keeps a second
 // CTA from being placed beside it (it would only wait in tcgen05.alloc).
 constexpr int kSmemFloor = 120 * 1024;
@@ -242,7 +244,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* p_full = s_full + 6;          // [2]
   uint64_t* o_done = p_full + 2;          // [2]
   uint64_t* o_full = o_done + 2;          // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + 2);
+  uint64_t* pv_done = o_full + 2;         // [2 groups][3 buffers]: P V has read the buffer's P
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 6);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -259,7 +262,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 6; ++i) mbar_init(&s_full[i], 1);
+    for (int i = 0; i < 6; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&pv_done[i], 1);
+    }
     for (int g = 0; g < 2; ++g) {
       mbar_init(&p_full[g], 4);
       mbar_init(&o_done[g], 1);
@@ -297,25 +303,31 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
     }
   } else if (warp == 1) {
-    {   // the whole warp walks the schedule (uniform operands); one elected lane issues
+    {   // scores S = Q K^T of tile j for both groups into buffer j % 3, once P V (j - 3) read it
       const uint32_t id_qk = make_idesc_bf16(128, 64, 0, 0);   // S[128 q][64 k] = Q K^T
-      const uint32_t id_pv = make_idesc_bf16(128, 64, 0, 1);   // O[128 q][64 d] += P V (V MN-major)
       bool ok = waitw(q_full, 0, kErrTimeoutFull);
-      auto qk = [&](int j) -> bool {
+      for (int j = 0; j < nkt && ok; ++j) {
         const int s = j % NSTAGE;
-        if (!waitw(&kv_full[s], (uint32_t)(j / NSTAGE) & 1u, kErrTimeoutFull)) return false;
-        tc_fence_after();
+        if (!waitw(&kv_full[s], (uint32_t)(j / NSTAGE) & 1u, kErrTimeoutFull)) { ok = false; break; }
         const uint64_t kd = kdesc0(smem_u32(sKV + s * 16384));
-        for (int g = 0; g < ngrp; ++g) {
+        for (int g = 0; g < ngrp && ok; ++g) {
+          if (j >= 3 && !waitw(&pv_done[3 * g + j % 3], (uint32_t)(((j / 3) - 1) & 1), kErrTimeoutOther)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
           const uint64_t qd = kdesc0(smem_u32(sQ + 16384 * g));
           const uint32_t tS = tbase + 256 * g + 64 * (j % 3);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_qk, kk > 0 ? 1u : 0u);
           umma_commit_w(&s_full[3 * g + (j % 3)]);
         }
-        return true;
-      };
-      for (int j = 0; j < 3 && j < nkt && ok; ++j) ok = qk(j);
+      }
+    }
+  } else if (warp == 10) {
+    {   // O += P V of tile j for each group once its P is in TMEM
+      const uint32_t id_pv = make_idesc_bf16(128, 64, 0, 1);   // O[128 q][64 d] += P V (V MN-major)
+      bool ok = true;
       for (int j = 0; j < nkt && ok; ++j) {
         const int s = j % NSTAGE;
         const uint64_t vd = mndesc0(smem_u32(sKV + s * 16384) + 8192);
@@ -327,14 +339,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           for (int kk = 0; kk < 4; ++kk)   // 64 keys = 4 k-steps; P at S columns [0, 32)
             umma_ts_w(tO, tS + kk * 8, mnstep(vd, kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit_w(&o_done[g]);
+          umma_commit_w(&pv_done[3 * g + j % 3]);
         }
-        if (!ok) break;
-        umma_commit_w(&kv_empty[s]);
-        if (j + 3 < nkt) ok = qk(j + 3);
+        // (the score MMAs of tile j completed before any P of it existed: K is free as well)
+        if (ok) umma_commit_w(&kv_empty[s]);
       }
       for (int g = 0; g < ngrp; ++g) umma_commit_w(&o_full[g]);
     }
-  } else {
+  } else {   // warps 2 .. 9
     // ------------------------------------------------------------ softmax + epilogue
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
@@ -500,7 +512,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* ds_full = s_full + 3;         // [3 buffers]
   uint64_t* acc_full = ds_full + 3;       // [2]
   uint64_t* acc_empty = acc_full + 2;     // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* dq_done = acc_empty + 2;      // [3 buffers]: the dQ MMA has read the buffer's dS
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_done + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -526,6 +539,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int i = 0; i < 3; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_full[i], 4);
+      mbar_init(&dq_done[i], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -571,14 +585,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         ++ii;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 10) {
     {   // the whole warp walks the schedule (uniform operands); one elected lane issues
       const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S = Q K^T, dP = dO V^T  [128 q][64 k]
       const uint32_t id_dq = make_idesc_bf16(128, 64, 0, 1);   // dQ[128 q][64 d] += dS K (K MN-major)
       bool ok = true;
-      // score cursor (runs up to three tiles ahead) and dQ cursor over the same tile stream; each
-      // rests on a key tile of an item that has some (the item counter ii, which picks the Q / dO
-      // buffer and the accumulator, counts only those items)
+      // a cursor over the key-tile stream, resting on a tile of an item that has some (the item
+      // counter ii, which picks the Q / dO / O buffer and the accumulator, counts only those)
       auto normalize = [&](ItemCursor& c, int& kt) {
         while (c.valid() && c.t0 == c.t1) { c.next(); if (c.valid()) kt = c.t0; }
       };
@@ -589,59 +602,61 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (c.valid()) kt = c.t0;
         normalize(c, kt);
       };
-      ItemCursor cs = cursor(), cd = cursor();
-      int ii_s = 0, kt_s = cs.valid() ? cs.t0 : 0, t_s = 0;
-      int ii_d = 0, kt_d = cd.valid() ? cd.t0 : 0, t_d = 0;
-      normalize(cs, kt_s);
-      normalize(cd, kt_d);
-      auto issue_sd = [&]() -> bool {
-        if (!cs.valid()) return true;
-        const int ib = ii_s & 1;
-        if (kt_s == cs.t0 && !waitw(&q_full[ib], (uint32_t)((ii_s >> 1) & 1), kErrTimeoutFull)) return false;
-        const int s = t_s % Q_STAGES;
-        if (!waitw(&kv_full[s], (uint32_t)(t_s / Q_STAGES) & 1u, kErrTimeoutFull)) return false;
-        tc_fence_after();
-        const uint32_t qa = smem_u32(sQd + 49152 * ib);
-        const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 16384);
-        const uint32_t ka = smem_u32(sKV + s * 16384), tS = tbase + 128 * (t_s % 3);
-        const uint64_t kd = kdesc0(ka), vd = kdesc0(ka + 8192);
+      ItemCursor c = cursor();
+      int ii = 0, kt = c.valid() ? c.t0 : 0, t = 0;
+      normalize(c, kt);
+      if (warp == 1) {
+        // scores: S = Q K^T and dP = dO V^T of tile t into buffer t % 3, once dQ(t - 3) has read it
+        while (ok && c.valid()) {
+          const int ib = ii & 1;
+          if (t >= 3 && !waitw(&dq_done[t % 3], (uint32_t)(((t / 3) - 1) & 1), kErrTimeoutOther)) { ok = false; break; }
+          if (kt == c.t0 && !waitw(&q_full[ib], (uint32_t)((ii >> 1) & 1), kErrTimeoutFull)) { ok = false; break; }
+          const int s = t % Q_STAGES;
+          if (!waitw(&kv_full[s], (uint32_t)(t / Q_STAGES) & 1u, kErrTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t qa = smem_u32(sQd + 49152 * ib);
+          const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 16384);
+          const uint32_t ka = smem_u32(sKV + s * 16384), tS = tbase + 128 * (t % 3);
+          const uint64_t kd = kdesc0(ka), vd = kdesc0(ka + 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
-        umma_commit_w(&s_full[t_s % 3]);
-        ++t_s;
-        advance(cs, ii_s, kt_s);
-        return true;
-      };
-      for (int i = 0; i < 3 && ok; ++i) ok = issue_sd();
-      while (ok) {
-        if (!cd.valid()) break;
-        const int ia = ii_d & 1;
-        const bool first = kt_d == cd.t0, last = kt_d + 1 == cd.t1;
-        if (!waitw(&ds_full[t_d % 3], (uint32_t)((t_d / 3) & 1), kErrTimeoutReady)) { ok = false; break; }
-        if (first && ii_d >= 2 && !waitw(&acc_empty[ia], (uint32_t)(((ii_d >> 1) - 1) & 1), kErrTimeoutOther)) {
-          ok = false;
-          break;
+          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
+          umma_commit_w(&s_full[t % 3]);
+          ++t;
+          advance(c, ii, kt);
         }
-        tc_fence_after();
-        const int s = t_d % Q_STAGES;
-        const uint64_t kmn = mndesc0(smem_u32(sKV + s * 16384));
-        const uint32_t tS = tbase + 128 * (t_d % 3), tQ = tbase + 384 + 64 * ia;
+      } else {
+        // gradient: dQ += dS K of tile t once its dS is in TMEM
+        while (ok && c.valid()) {
+          const int ia = ii & 1;
+          const bool first = kt == c.t0, last = kt + 1 == c.t1;
+          if (!waitw(&ds_full[t % 3], (uint32_t)((t / 3) & 1), kErrTimeoutReady)) { ok = false; break; }
+          if (first && ii >= 2 && !waitw(&acc_empty[ia], (uint32_t)(((ii >> 1) - 1) & 1), kErrTimeoutOther)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int s = t % Q_STAGES;
+          const uint64_t kmn = mndesc0(smem_u32(sKV + s * 16384));
+          const uint32_t tS = tbase + 128 * (t % 3), tQ = tbase + 384 + 64 * ia;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)   // 64 keys = 4 k-steps; dS at S columns [0, 32)
-          umma_ts_w(tQ, tS + kk * 8, mnstep(kmn, kk), id_dq, (!first || kk > 0) ? 1u : 0u);
-        umma_commit_w(&kv_empty[s]);
-        if (last) {
-          umma_commit_w(&acc_full[ia]);
-          umma_commit_w(&q_empty[ii_d & 1]);
+          for (int kk = 0; kk < 4; ++kk)   // 64 keys = 4 k-steps; dS at S columns [0, 32)
+            umma_ts_w(tQ, tS + kk * 8, mnstep(kmn, kk), id_dq, (!first || kk > 0) ? 1u : 0u);
+          // (the score MMAs of tile t completed before its dS existed, so these commits also
+          // cover their reads of K / V and of the item's Q / dO)
+          umma_commit_w(&dq_done[t % 3]);
+          umma_commit_w(&kv_empty[s]);
+          if (last) {
+            umma_commit_w(&acc_full[ia]);
+            umma_commit_w(&q_empty[ia]);
+          }
+          ++t;
+          advance(c, ii, kt);
         }
-        ++t_d;
-        advance(cd, ii_d, kt_d);
-        ok = issue_sd();
       }
     }
-  } else {
+  } else {   // warps 2 .. 9
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = 32 * quarter + lane;
@@ -800,7 +815,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint64_t* s_full = q_empty + NSTAGE;    // [3 buffers]
   uint64_t* ds_full = s_full + 3;         // [3 buffers]
   uint64_t* acc_full = ds_full + 3;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* gd_done = acc_full + 1;       // [3 buffers]: dV / dK MMAs have read the buffer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gd_done + 3);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -819,6 +835,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int i = 0; i < 3; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&ds_full[i], 4);
+      mbar_init(&gd_done[i], 1);
     }
     mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -854,14 +871,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       }
     }
   } else if (warp == 1) {
-    {   // the whole warp walks the schedule (uniform operands); one elected lane issues
-      const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S^T = K Q^T, dP^T = V dO^T  [128 k][64 q]
-      const uint32_t id_g = make_idesc_bf16(128, 64, 0, 1);    // dV / dK [128 k][64 d] (dO / Q MN-major)
+    {   // S^T = K Q^T and dP^T = V dO^T of query tile i into buffer i % 3, once dV / dK (i - 3) read it
+      const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S^T, dP^T [128 k][64 q]
       bool ok = waitw(kv_full, 0, kErrTimeoutFull);
       const uint64_t kd = kdesc0(smem_u32(sK)), vd = kdesc0(smem_u32(sV));
-      auto sd = [&](int i) -> bool {
+      for (int i = 0; i < nqt && ok; ++i) {
         const int s = i % NSTAGE;
-        if (!waitw(&q_full[s], (uint32_t)(i / NSTAGE) & 1u, kErrTimeoutFull)) return false;
+        if (i >= 3 && !waitw(&gd_done[i % 3], (uint32_t)(((i / 3) - 1) & 1), kErrTimeoutOther)) { ok = false; break; }
+        if (!waitw(&q_full[s], (uint32_t)(i / NSTAGE) & 1u, kErrTimeoutFull)) { ok = false; break; }
         tc_fence_after();
         const uint32_t qa = smem_u32(sQd + s * 16384), tS = tbase + 128 * (i % 3);
         const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 8192);
@@ -870,9 +887,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(vd, kk), kstep(dd, kk), id_s, kk > 0 ? 1u : 0u);
         umma_commit_w(&s_full[i % 3]);
-        return true;
-      };
-      for (int i = 0; i < 3 && i < nqt && ok; ++i) ok = sd(i);
+      }
+    }
+  } else if (warp == 10) {
+    {   // dV += P^T dO and dK += dS^T Q of query tile i once P^T / dS^T are in TMEM
+      const uint32_t id_g = make_idesc_bf16(128, 64, 0, 1);    // dV / dK [128 k][64 d] (dO / Q MN-major)
+      bool ok = true;
       for (int i = 0; i < nqt && ok; ++i) {
         const int s = i % NSTAGE;
         if (!waitw(&ds_full[i % 3], (uint32_t)((i / 3) & 1), kErrTimeoutReady)) { ok = false; break; }
@@ -885,12 +905,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)   // dS^T at dP^T columns [0, 32)
           umma_ts_w(tK, tS + 64 + kk * 8, mnstep(qmn, kk), id_g, (i > 0 || kk > 0) ? 1u : 0u);
+        // (the score MMAs of tile i completed before its P^T existed: Q / dO are free as well)
+        umma_commit_w(&gd_done[i % 3]);
         umma_commit_w(&q_empty[s]);
-        if (i + 3 < nqt) ok = sd(i + 3);
       }
       umma_commit_w(acc_full);
     }
-  } else {
+  } else {   // warps 2 .. 9
     const int g = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = 32 * quarter + lane;
