@@ -87,10 +87,23 @@ __global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float
   }
 }
 
-// RoPE angle of pair i (< rot/2) at position pos: pos * base^(-2i/rot)
-__device__ __forceinline__ void rope_cs(int pos, int i, int rot, float log2_base, float& c, float& s) {
+// RoPE angle of pair i (< rot/2) at position pos: pos * base^(-2i/rot); its (cos, sin) come from
+// a table built once per (positions, rot, base) rather than from sincos in every warp.
+__global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __restrict__ tab) {
+  const int half = rot / 2;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (e >= tps * half) return;
+  const int pos = e / half, i = e % half;
   const float freq = exp2f(-2.0f * (float)i / (float)rot * log2_base);
-  sincosf((float)pos * freq, &s, &c);
+  float sn, cs;
+  sincosf((float)pos * freq, &sn, &cs);
+  tab[e] = make_float2(cs, sn);
+}
+
+__device__ __forceinline__ void rope_cs(const float2* __restrict__ tab, int pos, int i, int rot, float& c, float& s) {
+  const float2 v = tab[pos * (rot / 2) + i];
+  c = v.x;
+  s = v.y;
 }
 
 // One warp per (token, head, slice); lane l holds head elements l and l + 32.
@@ -100,7 +113,8 @@ struct HeadSlices {
 };
 
 __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
-                                     int tps, float eps, int rot, float log2_base, __nv_bfloat16* __restrict__ out) {
+                                     int tps, float eps, int rot, const float2* __restrict__ tab,
+                                     __nv_bfloat16* __restrict__ out) {
   const int nslices = slices.n;
   const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const long total = (long)T * H * nslices;
@@ -123,11 +137,11 @@ __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int nco
     if (rot == 32) {   // pairs (i, i + 16) for i < 16 live in lanes i and i ^ 16
       const float pa = __shfl_xor_sync(0xffffffffu, a, 16);
       float c, s;
-      rope_cs(pos, lane & 15, rot, log2_base, c, s);
+      rope_cs(tab, pos, lane & 15, rot, c, s);
       a = lane < 16 ? a * c - pa * s : pa * s + a * c;
     } else if (rot == 64) {   // pairs (i, i + 32) live in one lane
       float c, s;
-      rope_cs(pos, lane, rot, log2_base, c, s);
+      rope_cs(tab, pos, lane, rot, c, s);
       const float na = a * c - b * s, nb = a * s + b * c;
       a = na;
       b = nb;
@@ -138,8 +152,8 @@ __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int nco
 }
 
 __global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, const float* __restrict__ y, int T,
-                                     int ncols, int H, HeadSlice sl, int tps, int rot, float log2_base,
-                                     float* __restrict__ dy) {
+                                     int ncols, int H, HeadSlice sl, int tps, int rot,
+                                     const float2* __restrict__ tab, float* __restrict__ dy) {
   const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (wid >= (long)T * H) return;
   const int lane = threadIdx.x & 31;
@@ -151,11 +165,11 @@ __global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, con
     if (rot == 32) {
       const float pa = __shfl_xor_sync(0xffffffffu, ga, 16);
       float c, s;
-      rope_cs(pos, lane & 15, rot, log2_base, c, s);
+      rope_cs(tab, pos, lane & 15, rot, c, s);
       ga = lane < 16 ? ga * c + pa * s : -pa * s + ga * c;
     } else if (rot == 64) {
       float c, s;
-      rope_cs(pos, lane, rot, log2_base, c, s);
+      rope_cs(tab, pos, lane, rot, c, s);
       const float na = ga * c + gb * s, nb = -ga * s + gb * c;
       ga = na;
       gb = nb;
@@ -205,24 +219,42 @@ __global__ void add_kernel(const float* __restrict__ x, const float* __restrict_
 
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
 
+// SwiGLU over rows: f[t] = [val (I) | gate (I)], a[t] = val * silu(gate).  Grid (I / 4 / 256
+// column blocks, T rows): each thread owns 4 consecutive columns of one row (128-bit accesses).
 __global__ void swiglu_fwd_kernel(const float* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
-  const long n = (long)T * I;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long t = i / I, j = i % I;
-    const float v = f[t * 2 * I + j], gl = f[t * 2 * I + I + j];
-    a[i] = __float2bfloat16_rn(v * gl * sigm(gl));
+  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (j >= I) return;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+  const float* fr = f + (long)t * 2 * I;
+  const float4 v = *reinterpret_cast<const float4*>(fr + j);
+  const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
+  uint2 pk;
+  pk.x = pack_bf16x2(v.x * gl.x * sigm(gl.x), v.y * gl.y * sigm(gl.y));
+  pk.y = pack_bf16x2(v.z * gl.z * sigm(gl.z), v.w * gl.w * sigm(gl.w));
+  *reinterpret_cast<uint2*>(a + (long)t * I + j) = pk;
   }
 }
 
 __global__ void swiglu_bwd_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
                                   float* __restrict__ df) {
-  const long n = (long)T * I;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long t = i / I, j = i % I;
-    const float v = f[t * 2 * I + j], gl = f[t * 2 * I + I + j];
-    const float sg = sigm(gl), d = da[i];
-    df[t * 2 * I + j] = d * gl * sg;
-    df[t * 2 * I + I + j] = d * v * sg * (1.f + gl * (1.f - sg));
+  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (j >= I) return;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+  const float* fr = f + (long)t * 2 * I;
+  const float4 v = *reinterpret_cast<const float4*>(fr + j);
+  const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
+  const float4 d = *reinterpret_cast<const float4*>(da + (long)t * I + j);
+  const float vv[4] = {v.x, v.y, v.z, v.w}, gg[4] = {gl.x, gl.y, gl.z, gl.w}, dd[4] = {d.x, d.y, d.z, d.w};
+  float dv[4], dgl[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float sg = sigm(gg[e]);
+    dv[e] = dd[e] * gg[e] * sg;
+    dgl[e] = dd[e] * vv[e] * sg * (1.f + gg[e] * (1.f - sg));
+  }
+  float* dr = df + (long)t * 2 * I;
+  *reinterpret_cast<float4*>(dr + j) = make_float4(dv[0], dv[1], dv[2], dv[3]);
+  *reinterpret_cast<float4*>(dr + I + j) = make_float4(dgl[0], dgl[1], dgl[2], dgl[3]);
   }
 }
 
@@ -302,26 +334,55 @@ int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd
   return check_launch("rmsnorm_mod_bwd", err);
 }
 
+// (cos, sin) table of the context for (tps, rot, base); rebuilt only when one of them changes
+static const float2* rope_table(Ctx* c, int tps, int rot, float rope_base, std::string& err) {
+  if (rot == 0) return nullptr;
+  const size_t bytes = sizeof(float2) * (size_t)tps * (rot / 2);
+  void* tab = scratch_get(c, kSlotRope, bytes, err);
+  if (!tab) return nullptr;
+  if (tab != c->rope_tab || c->rope_tps != tps || c->rope_rot != rot || c->rope_base != rope_base) {
+    const int n = tps * (rot / 2);
+    rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(tps, rot, log2f(rope_base),
+                                                                            static_cast<float2*>(tab));
+    if (check_launch("rope table", err)) return nullptr;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(c->stream, &cs);
+    if (cs == cudaStreamCaptureStatusNone) {   // a captured build only exists once the graph runs
+      c->rope_tab = tab;
+      c->rope_tps = tps;
+      c->rope_rot = rot;
+      c->rope_base = rope_base;
+    }
+  }
+  return static_cast<const float2*>(tab);
+}
+
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
                     float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
   if (rot != 0 && rot != 32 && rot != 64) { err = "rope: rot must be 32 or 64"; return 1; }
   if (nslices < 1 || nslices > 5) { err = "head_prep: 1..5 slices"; return 1; }
   HeadSlices hs{};
-  for (int i = 0; i < nslices; ++i) hs.s[i] = slices[i];
+  bool any_rope = false;
+  for (int i = 0; i < nslices; ++i) {
+    hs.s[i] = slices[i];
+    any_rope = any_rope || slices[i].rope;
+  }
   hs.n = nslices;
+  const float2* tab = nullptr;
+  if (any_rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
   const long warps = (long)T * H * nslices;
-  head_prep_fwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot,
-                                                                           log2f(rope_base), out);
+  head_prep_fwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
 
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
                     int tps, int rot, float rope_base, float* dy, std::string& err) {
+  const float2* tab = nullptr;
+  if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
   const long warps = (long)T * H;
-  head_prep_bwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot,
-                                                                           log2f(rope_base), dy);
+  head_prep_bwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
   return check_launch("head_prep_bwd", err);
 }
 
@@ -347,13 +408,15 @@ int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::strin
 
 int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err) {
   ProfScope prof_(c, "swiglu_fwd");
-  swiglu_fwd_kernel<<<gs((long)T * I), 256, 0, c->stream>>>(f, T, I, a);
+  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
+  swiglu_fwd_kernel<<<dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(f, T, I, a);
   return check_launch("swiglu_fwd", err);
 }
 
 int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err) {
   ProfScope prof_(c, "swiglu_bwd");
-  swiglu_bwd_kernel<<<gs((long)T * I), 256, 0, c->stream>>>(da, f, T, I, df);
+  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
+  swiglu_bwd_kernel<<<dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(da, f, T, I, df);
   return check_launch("swiglu_bwd", err);
 }
 

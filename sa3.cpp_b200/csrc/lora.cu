@@ -166,17 +166,22 @@ __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* _
 //   dB[o][r] += dt2 P[o][r] + 2 dt3 (B AAt)[o][r]
 //   cb[r][o] = bf16(dt2 B[o][r])   (A operand of dA += cb W, a rank-16 quant GEMM)
 //   c3[r][k] += dt3 B[o][r] B[o][k]           (dA += 2 c3 A afterwards)
-__global__ void dora_bwd_kernel(const float* __restrict__ pt, const float* __restrict__ B, int rank,
-                                int64_t out, const float* __restrict__ aat, const float* __restrict__ nsq,
-                                const float* __restrict__ g, const float* __restrict__ dg, float s,
-                                float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB,
-                                __nv_bfloat16* __restrict__ cb, float* __restrict__ c3) {
+// 128 rows per block.  Phase 1: one thread per row (dm, dB, cb; the row's dt3 B[o][:] and B[o][:]
+// go to shared memory).  Phase 2: thread (r, k), r <= k < R, sums dt3 B[o][r] B[o][k] over the
+// block's rows and adds it to c3 (one atomic per entry and block).
+constexpr int kDoraRows = 128;
+__global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
+    const float* __restrict__ pt, const float* __restrict__ B, int rank, int64_t out, const float* __restrict__ aat,
+    const float* __restrict__ nsq, const float* __restrict__ g, const float* __restrict__ dg, float s,
+    float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __nv_bfloat16* __restrict__ cb,
+    float* __restrict__ c3) {
   __shared__ float saat[R * R];
-  __shared__ float sc3[R * R];
-  saat[threadIdx.x % (R * R)] = aat[threadIdx.x % (R * R)];
-  sc3[threadIdx.x % (R * R)] = 0.f;
+  __shared__ float sb[kDoraRows][R + 1];    // B[o][:]          (+1: no bank conflicts on columns)
+  __shared__ float sbt[kDoraRows][R + 1];   // dt3[o] B[o][:]
+  for (int e = threadIdx.x; e < R * R; e += blockDim.x) saat[e] = aat[e];
   __syncthreads();
-  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = threadIdx.x;
+  const int64_t o = (int64_t)blockIdx.x * kDoraRows + row;
   float b[R];
   float dt3 = 0.f;
 #pragma unroll
@@ -199,23 +204,24 @@ __global__ void dora_bwd_kernel(const float* __restrict__ pt, const float* __res
       cb[(int64_t)r * out + o] = __float2bfloat16_rn(dt2 * b[r]);
     }
   }
-  // c3 = B^T diag(dt3) B over this block's rows: warp sums, then one shared atomic per warp.
-  // Fully unrolled over the padded rank (b is zero beyond `rank`) so b stays in registers.
-  const int lane = threadIdx.x & 31;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    const float br = dt3 * b[r];
-#pragma unroll
-    for (int k = r; k < R; ++k) {
-      const float v = warp_sum(br * b[k]);
-      if (lane == 0 && r < rank && k < rank) {
-        atomicAdd(&sc3[r * R + k], v);
-        if (k != r) atomicAdd(&sc3[k * R + r], v);
-      }
-    }
+    sb[row][r] = b[r];
+    sbt[row][r] = dt3 * b[r];
   }
   __syncthreads();
-  if (threadIdx.x < R * R && sc3[threadIdx.x] != 0.f) atomicAdd(c3 + threadIdx.x, sc3[threadIdx.x]);
+  // 136 (r <= k) entries of the symmetric R x R block sum
+  const int nrows = (int)min((int64_t)kDoraRows, out - (int64_t)blockIdx.x * kDoraRows);
+  for (int e = threadIdx.x; e < R * (R + 1) / 2; e += blockDim.x) {
+    int r = 0, rem = e;
+    while (rem >= R - r) { rem -= R - r; ++r; }
+    const int k = r + rem;
+    if (r >= rank || k >= rank) continue;
+    float acc = 0.f;
+    for (int q = 0; q < nrows; ++q) acc = fmaf(sbt[q][r], sb[q][k], acc);
+    atomicAdd(c3 + r * R + k, acc);
+    if (k != r) atomicAdd(c3 + k * R + r, acc);
+  }
 }
 
 // dA[r][i] += 2 sum_k c3[r][k] A[k][i]
@@ -287,8 +293,8 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
                float* dB, __nv_bfloat16* cb, float* c3, std::string& err) {
   ProfScope prof_(c, "dora_bwd");
-  dora_bwd_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, nsq, g, dg, s, dm,
-                                                                       dm_acc, dB, cb, c3);
+  dora_bwd_kernel<<<(unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, c->stream>>>(
+      pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_acc, dB, cb, c3);
   return check_launch("dora_bwd", err);
 }
 

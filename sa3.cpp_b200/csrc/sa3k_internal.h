@@ -59,6 +59,10 @@ struct Ctx {
   int tile_n = 0;                    // main-GEMM N tile: 0 = cost model, 128 or 256 = fixed
   bool gemm_pair = true;             // CTA-pair (cta_group::2) GEMMs where they fit
   bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
+  // NeoX RoPE (cos, sin) table for (positions, rot, base), kept in scratch slot kSlotRope
+  const void* rope_tab = nullptr;
+  int rope_tps = 0, rope_rot = 0;
+  float rope_base = 0.f;
   std::vector<ProfEntry> prof;
   std::vector<cudaEvent_t> ev_pool;
 };
@@ -90,7 +94,7 @@ inline int check_launch(const char* what, std::string& err) {
 }
 
 // Scratch slots owned by a context (see api.cu for the linear path's slots).
-enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62 };
+enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61 };
 
 // Scratch slot `slot` of at least `bytes` (grows; contents are not preserved on growth).
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
