@@ -23,6 +23,7 @@
 #include "linear.h"
 #include "lora_kernels.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -68,6 +69,8 @@ struct DitModel {
   float *p = nullptr, *g = nullptr, *am = nullptr, *av = nullptr;
   int64_t np = 0;
   void* prep_mem = nullptr;
+  PrepDesc* prep_desc = nullptr;       // device descriptors of the adapters (grouped preparation)
+  int64_t max_out = 0;
   // activations for shape (B, T, C)
   int B = 0, T = 0, C = 0;
   void* arena = nullptr;
@@ -237,9 +240,16 @@ static int dit_step(DitModel& m, std::string& err) {
   const float scale = 1.0f / std::sqrt((float)k.head_dim);
   if (k.differential) { err = "differential attention is not supported by the training step yet"; return 1; }
 
-  // adapters: operand forms + DoRA norms, once per step
-  for (DitTarget& t : m.tg)
-    if (adapter_prepare(c, t.w, t.prep, err)) return 1;
+  // adapters: operand forms + DoRA norms, once per step (grouped launches over all adapters; the
+  // DoRA P = W A^T GEMMs run per adapter between them)
+  const int nt = (int)m.tg.size();
+  if (k_prep_all(c, m.prep_desc, nt, err)) return 1;
+  if (m.dora) {
+    if (k_aat_all(c, m.prep_desc, nt, err)) return 1;
+    for (DitTarget& t : m.tg)
+      if (adapter_dora_p(c, t.w, t.prep, err)) return 1;
+    if (k_dora_norm_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
+  }
 
   // ---------------- head (src/dit.h:286-310)
   if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
@@ -554,6 +564,22 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     adapter_bind(p, pm);
     pm += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
   }
+  // device descriptors of all adapters for the grouped preparation kernels of every step
+  std::vector<PrepDesc> descs;
+  for (DitTarget& t : m.tg) {
+    const AdapterPrep& p = t.prep;
+    PrepDesc pd{};
+    pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
+    pd.rank = p.rank; pd.dora = p.dora() ? 1 : 0; pd.s = p.s; pd.in = p.in; pd.out = p.out;
+    pd.a_bf = p.a_bf; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_bf = p.bt_bf;
+    pd.pt = p.pt; pd.aat = p.aat; pd.nsq = p.nsq; pd.g = p.g;
+    descs.push_back(pd);
+    m.max_out = std::max(m.max_out, p.out);
+  }
+  m.prep_desc = static_cast<PrepDesc*>(dmalloc(m, sizeof(PrepDesc) * descs.size(), e));
+  if (!m.prep_desc) return dfail(err, err_len, e);
+  if (cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+    return dfail(err, err_len, "adapter descriptor upload failed");
   if (cudaStreamSynchronize(m.c->stream) != cudaSuccess) return dfail(err, err_len, "adapter init failed");
   return 0;
 }

@@ -76,11 +76,22 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
     if (splits > 1) {
       const int kps = (nkb + splits - 1) / splits;
       splits = (nkb + kps - 1) / kps;
-      float* part = static_cast<float*>(scratch_get(c, kSlotSplitK, (size_t)splits * d.M * d.N * sizeof(float), err));
-      if (!part) return 1;
       a.splits = splits;
       a.kb_per_split = kps;
-      a.partial = part;
+      if (d.atomic_split && d.out && !d.out_bf) {
+        // the splits add into `out` directly; without accumulation it starts from zero
+        a.atomic = 1;
+        if (!d.accumulate) {
+          const size_t rows = d.out_trans ? (size_t)d.N : (size_t)d.M, cols = d.out_trans ? (size_t)d.M : (size_t)d.N;
+          if (cudaMemset2DAsync(d.out, (size_t)d.ldo * sizeof(float), 0, cols * sizeof(float), rows, c->stream) !=
+              cudaSuccess)
+            return check_launch("gemm atomic split-K memset", err);
+        }
+      } else {
+        float* part = static_cast<float*>(scratch_get(c, kSlotSplitK, (size_t)splits * d.M * d.N * sizeof(float), err));
+        if (!part) return 1;
+        a.partial = part;
+      }
     }
   }
   // epilogue through TMA stores when the output is a single row-major tensor
@@ -104,7 +115,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
     kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, tout, a);
     if (check_launch("gemm_tc", err)) return 1;
   }
-  if (a.splits > 1) {
+  if (a.splits > 1 && !a.atomic) {
     ProfScope prof_(c, "splitk_reduce");
     const long mn = (long)d.M * d.N;
     long blocks = (mn + 255) / 256;
@@ -291,6 +302,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.kb_per_split = 1;
   a.partial = nullptr;
   a.tma_out = 0;
+  a.atomic = 0;
 
   if (bn == 16) {
     if (bmode != 0) { err = "gemm: N tile 16 supports bf16 K-major B only"; return 1; }

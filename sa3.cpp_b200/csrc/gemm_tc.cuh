@@ -51,6 +51,7 @@ struct GemmArgs {
   float* partial;           // split-K: raw f32 partial sums [splits][M][N] (epilogue deferred)
   int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: bf16 `out_bf` via TMA
                             //    store; 0: direct stores (split-K partials, transposed or dual outputs)
+  int atomic;               // split-K: every split adds its (scaled) part into `out` with atomics
   int* err;                 // device error word
 };
 
@@ -203,8 +204,8 @@ __global__ void splitk_reduce_kernel(const GemmArgs args) {
 // (raw sums for split-K partials).  Column vectors are read 4 at a time (the same addresses for
 // every lane of the warp: broadcast loads).
 __device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, int n0, const GemmArgs& args,
-                                            bool raw) {
-  if (raw || !(args.col_scale || args.col_bias)) {
+                                            bool raw, const float* col_bias) {
+  if (raw || !(args.col_scale || col_bias)) {
     const float al = raw ? 1.f : args.alpha;
 #pragma unroll
     for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]) * al + 0.f;
@@ -213,7 +214,7 @@ __device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, i
     for (int j = 0; j < 32; j += 4) {
       float4 s4 = make_float4(1.f, 1.f, 1.f, 1.f), b4 = make_float4(0.f, 0.f, 0.f, 0.f);
       if (args.col_scale) s4 = __ldg(reinterpret_cast<const float4*>(args.col_scale + n0 + j));
-      if (args.col_bias) b4 = __ldg(reinterpret_cast<const float4*>(args.col_bias + n0 + j));
+      if (col_bias) b4 = __ldg(reinterpret_cast<const float4*>(col_bias + n0 + j));
       f[j] = __uint_as_float(v[j]) * (args.alpha * s4.x) + b4.x;
       f[j + 1] = __uint_as_float(v[j + 1]) * (args.alpha * s4.y) + b4.y;
       f[j + 2] = __uint_as_float(v[j + 2]) * (args.alpha * s4.z) + b4.z;
@@ -226,7 +227,7 @@ __device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, i
       float cs = args.alpha, cb = 0.f;
       if (n < args.N) {
         if (args.col_scale) cs *= args.col_scale[n];
-        if (args.col_bias) cb = args.col_bias[n];
+        if (col_bias) cb = col_bias[n];
       }
       f[j] = __uint_as_float(v[j]) * cs + cb;
     }
@@ -424,7 +425,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     // is one coalesced row segment; transposed outputs are already coalesced across lanes.
     const int q = warp & 3;   // TMEM lane quarter this warp may access
     uint8_t* stg = smem + L::OFF_STAGE + (warp - 2) * L::STAGE_BUFS * L::STAGE_BYTES;
-    const bool split_out = args.partial != nullptr;
+    const bool split_out = args.partial != nullptr;   // raw partial sums (reduced by a second pass)
     const int cstep = args.tma_out == 2 ? 64 : 32;
     int nstore = 0;
     int ti = 0;
@@ -452,7 +453,9 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             tmem_ld16(tacc + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           }
           tmem_ld_wait();
-          epi_columns(v, f + 32 * h, nb + 32 * h, args, split_out);
+          // with atomic split-K every split adds its scaled part; only split 0 adds the bias
+          epi_columns(v, f + 32 * h, nb + 32 * h, args, split_out,
+                      (args.atomic && item >= ntiles) ? nullptr : args.col_bias);
         }
         if (!have || nb >= args.N) continue;
         if (args.tma_out) {
@@ -501,7 +504,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             for (int j = 0; j < 32; ++j) {   // static indices keep f[] in registers
               if (j >= ncols) break;
               float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
-              *dst = args.accumulate ? *dst + f[j] : f[j];
+              if (args.atomic) atomicAdd(dst, f[j]);
+              else *dst = args.accumulate ? *dst + f[j] : f[j];
             }
           }
         }
@@ -530,7 +534,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             }
             if (args.out && !args.out_trans) {
               float* dst = args.out + (long)row * args.ldo + nb + lane;
-              *dst = args.accumulate ? *dst + x : x;
+              if (args.atomic) atomicAdd(dst, x);
+              else *dst = args.accumulate ? *dst + x : x;
             }
             if (args.out_bf && !args.out_bf_trans) args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x);
           }

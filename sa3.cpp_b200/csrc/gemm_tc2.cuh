@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(192, 1)
           uint32_t v[32];
           tmem_ld32(tacc + (uint32_t)(c0 + 32 * h), v);
           tmem_ld_wait();
-          epi_columns(v, f + 32 * h, nb + 32 * h, args, false);
+          epi_columns(v, f + 32 * h, nb + 32 * h, args, false, args.col_bias);
         }
         if (!have || nb >= args.N) continue;
         if (args.tma_out) {

@@ -39,16 +39,27 @@ void adapter_bind(AdapterPrep& p, void* mem) {
   }
 }
 
+int adapter_dora_p(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
+  GemmDesc g;
+  if (w->bf16) {   // P = W A^T [out][16] with out as M, stored transposed as P^T [16][out]
+    g.M = (int)p.out; g.N = 16; g.K = (int)p.in;
+    g.a = w->bf16; g.lda = p.in;
+    g.bsrc = kB_BF16_KMAJOR; g.b = p.a_bf; g.ldb = p.in;
+    g.out = p.pt; g.ldo = p.out; g.out_trans = 1; g.bn = 16;
+  } else {         // quantized base without an operand copy: P^T = A W^T [16][out]
+    g.M = 16; g.N = (int)p.out; g.K = (int)p.in;
+    g.a = p.a_bf; g.lda = p.in;
+    g.bsrc = kB_WEIGHT_NT; g.w = w;
+    g.out = p.pt; g.ldo = p.out;
+  }
+  g.name = "dora.P";
+  return gemm(c, g, err);
+}
+
 int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
   if (k_prep_adapter(c, p.A, p.B, p.rank, p.in, p.out, p.a_bf, p.at_x, p.b_x, p.bt_bf, err)) return 1;
   if (!p.dora()) return 0;
-  GemmDesc g;   // P^T = A W^T  [16][out]
-  g.M = 16; g.N = (int)p.out; g.K = (int)p.in;
-  g.a = p.a_bf; g.lda = p.in;
-  g.bsrc = kB_WEIGHT_NT; g.w = w;
-  g.out = p.pt; g.ldo = p.out;
-  g.name = "dora.P";
-  if (gemm(c, g, err)) return 1;
+  if (adapter_dora_p(c, w, p, err)) return 1;
   if (k_aat(c, p.A, p.rank, p.in, p.aat, err)) return 1;
   return k_dora_norm(c, p.pt, p.B, p.rank, p.out, p.aat, p.bns, p.m, p.s, p.nsq, p.g, err);
 }
@@ -113,6 +124,8 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
     if (gemm(c, g, err)) return 1;
   }
   if (!ad) return 0;
+  // The rank-16 gradient GEMMs run with the long dimension as M (full 128-row MMA tiles) and
+  // add their split-K parts into the gradient with atomics.
   {
     GemmDesc g;   // dB = s dz^T u  [out][rank]
     g.M = (int)out; g.N = rank; g.K = (int)b.M;
@@ -120,15 +133,17 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
     g.bsrc = kB_BF16_KMAJOR; g.b = b.ut; g.ldb = b.ut_ld;
     g.alpha = ad->s;
     g.out = b.dB; g.ldo = rank; g.accumulate = b.grad_accumulate; g.bn = 16;
+    g.atomic_split = 1;
     g.name = "lora.dB";
     if (gemm(c, g, err)) return 1;
   }
   {
-    GemmDesc g;   // dA = du^T x  [rank][in]
-    g.M = rank; g.N = (int)in; g.K = (int)b.M;
-    g.a = b.dut; g.lda = b.ut_ld;
-    g.bsrc = kB_BF16_MNMAJOR; g.b = b.x_bf; g.ldb = in;
-    g.out = b.dA; g.ldo = in; g.accumulate = b.grad_accumulate;
+    GemmDesc g;   // dA^T = x^T du  [in][rank], stored transposed as dA [rank][in]
+    g.M = (int)in; g.N = rank; g.K = (int)b.M;
+    g.a = b.x_bf; g.lda = in; g.a_mn = 1;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.dut; g.ldb = b.ut_ld;
+    g.out = b.dA; g.ldo = in; g.out_trans = 1; g.accumulate = b.grad_accumulate; g.bn = 16;
+    g.atomic_split = 1;
     g.name = "lora.dA";
     if (gemm(c, g, err)) return 1;
   }
@@ -138,10 +153,18 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
                  b.cb, b.c3, err))
     return 1;
   GemmDesc g;   // dA += (dt2 B)^T W
-  g.M = rank; g.N = (int)in; g.K = (int)out;
-  g.a = b.cb; g.lda = out;
-  g.bsrc = kB_WEIGHT_TN; g.w = w;
-  g.out = b.dA; g.ldo = in; g.accumulate = 1;
+  if (w->bf16) {   // as dA^T += W^T (dt2 B): the bf16 operand copy read MN-major
+    g.M = (int)in; g.N = rank; g.K = (int)out;
+    g.a = w->bf16; g.lda = in; g.a_mn = 1;
+    g.bsrc = kB_BF16_KMAJOR; g.b = b.cb; g.ldb = out;
+    g.out = b.dA; g.ldo = in; g.out_trans = 1; g.accumulate = 1; g.bn = 16;
+    g.atomic_split = 1;
+  } else {         // quantized base without an operand copy: W^T dequantized in the GEMM
+    g.M = rank; g.N = (int)in; g.K = (int)out;
+    g.a = b.cb; g.lda = out;
+    g.bsrc = kB_WEIGHT_TN; g.w = w;
+    g.out = b.dA; g.ldo = in; g.accumulate = 1;
+  }
   g.name = "dora.dA";
   if (gemm(c, g, err)) return 1;
   return k_dora_da_c3(c, b.c3, ad->A, rank, in, b.dA, err);

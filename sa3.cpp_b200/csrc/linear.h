@@ -31,6 +31,9 @@ struct AdapterPrep {
 size_t adapter_prep_bytes(int64_t in, int64_t out, bool dora);
 void adapter_bind(AdapterPrep& p, void* mem);
 int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err);
+// The DoRA P = W A^T GEMM of one adapter (its part of adapter_prepare between the grouped
+// packing and the grouped norm).
+int adapter_dora_p(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err);
 
 struct LinearFwd {
   const Weight* w = nullptr;

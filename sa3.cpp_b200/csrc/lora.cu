@@ -134,6 +134,82 @@ __global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __re
   g[o] = m[o] / sqrtf(n2);
 }
 
+// ---------------------------------------------------------------- grouped adapter preparation
+// The same three preparations for every adapter of a model in one launch each (grid.y = adapter),
+// driven by a device array of PrepDesc built once when the adapters are bound.
+__global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
+  const PrepDesc d = descs[blockIdx.y];
+  const int stride = gridDim.x * blockDim.x;
+  const int t0 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int nin = (int)d.in * 64, nout = (int)d.out * 64;
+  for (int k = t0; k < nin; k += stride) {
+    const int i = k >> 6, c = k & 63;
+    const float a = (c < d.rank) ? d.A[(int64_t)c * d.in + i] : 0.f;
+    d.at_x[k] = __float2bfloat16_rn(a);
+    if (c < R) d.a_bf[(int64_t)c * d.in + i] = __float2bfloat16_rn(a);
+  }
+  for (int k = t0; k < nout; k += stride) {
+    const int o = k >> 6, c = k & 63;
+    const float b = (c < d.rank) ? d.B[(int64_t)o * d.rank + c] : 0.f;
+    d.b_x[k] = __float2bfloat16_rn(b);
+    if (c < R) d.bt_bf[(int64_t)c * d.out + o] = __float2bfloat16_rn(b);
+  }
+}
+
+__global__ void aat_all_kernel(const PrepDesc* __restrict__ descs) {
+  const PrepDesc d = descs[blockIdx.y];
+  if (!d.dora) return;
+  const int r1 = blockIdx.x;
+  float acc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) acc[r] = 0.f;
+  if (r1 < d.rank) {
+    for (int64_t i = threadIdx.x; i < d.in; i += blockDim.x) {
+      const float a1 = d.A[(int64_t)r1 * d.in + i];
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[r] = r < d.rank ? fmaf(a1, d.A[(int64_t)r * d.in + i], acc[r]) : 0.f;
+    }
+  }
+  __shared__ float part[8][R];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const float v = warp_sum(acc[r]);
+    if (lane == 0) part[wid][r] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < R) {
+    float v = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += part[w][threadIdx.x];
+    d.aat[r1 * R + threadIdx.x] = v;
+  }
+}
+
+__global__ void dora_norm_all_kernel(const PrepDesc* __restrict__ descs) {
+  const PrepDesc d = descs[blockIdx.y];
+  if (!d.dora) return;
+  __shared__ float saat[R * R];
+  saat[threadIdx.x % (R * R)] = d.aat[threadIdx.x % (R * R)];
+  __syncthreads();
+  const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= d.out) return;
+  float b[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) b[r] = r < d.rank ? d.B[o * d.rank + r] : 0.f;
+  float t2 = 0.f, t3 = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    t2 = fmaf(d.pt[(int64_t)r * d.out + o], b[r], t2);
+    float bar = 0.f;
+#pragma unroll
+    for (int k = 0; k < R; ++k) bar = fmaf(b[k], saat[k * R + r], bar);
+    t3 = fmaf(bar, b[r], t3);
+  }
+  const float n2 = d.bns[o] + 2.f * d.s * t2 + d.s * d.s * t3;
+  d.nsq[o] = n2;
+  d.g[o] = d.m[o] / sqrtf(n2);
+}
+
 // Backward prologue over dy[S][out] (one thread per column, TOK rows per block):
 //   dz = bf16(g * dy) ;  dg[o] += sum_t dy[t][o] * (y[t][o] - bias[o]) / g[o]   (dora only)
 // With g == null this is the plain f32 -> bf16 conversion of dy.
@@ -296,6 +372,24 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
   dora_bwd_kernel<<<(unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, c->stream>>>(
       pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_acc, dB, cb, c3);
   return check_launch("dora_bwd", err);
+}
+
+int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
+  ProfScope prof_(c, "prep_adapter");
+  prep_all_kernel<<<dim3(48, (unsigned)n), 256, 0, c->stream>>>(descs);
+  return check_launch("prep_all", err);
+}
+
+int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
+  ProfScope prof_(c, "aat");
+  aat_all_kernel<<<dim3(R, (unsigned)n), 256, 0, c->stream>>>(descs);
+  return check_launch("aat_all", err);
+}
+
+int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err) {
+  ProfScope prof_(c, "dora_norm");
+  dora_norm_all_kernel<<<dim3((unsigned)((max_out + 255) / 256), (unsigned)n), 256, 0, c->stream>>>(descs);
+  return check_launch("dora_norm_all", err);
 }
 
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err) {

@@ -5,7 +5,24 @@
 
 namespace sa3k {
 
+// One adapter's preparation inputs and outputs (device pointers), for the grouped kernels.
+struct PrepDesc {
+  const float* A;      // [rank][in]
+  const float* B;      // [out][rank]
+  const float* m;      // [out] (dora)
+  const float* bns;    // [out] (dora)
+  int rank, dora;
+  float s;
+  int64_t in, out;
+  __nv_bfloat16 *a_bf, *at_x, *b_x, *bt_bf;
+  float *pt, *aat, *nsq, *g;
+};
+
 int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err);
+// grouped over n adapters (descs in device memory): operand packing, A A^T, DoRA norm
+int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
+int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
+int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
 int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
                 __nv_bfloat16* trans, int ld_trans, std::string& err);
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,

@@ -139,6 +139,9 @@ struct GemmDesc {
   long ldo_bf = 0;
   int out_bf_trans = 0;
   int bn = 128;         // N tile (16, 128)
+  // split-K partial sums may be added into `out` with f32 atomics (no reduction pass; the
+  // summation order, and so the last bits, vary from run to run).  f32 `out` only.
+  int atomic_split = 0;
   const char* name = "gemm";   // launch class for the profiler
 };
 
