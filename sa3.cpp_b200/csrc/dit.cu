@@ -197,11 +197,13 @@ static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float
   return linear_forward(m.c, f, err);
 }
 
+// dy == nullptr: m.dz (and m.dg for dora) were written by a fused producer of the gradient
 static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
                    const float* y, const float* dy, int64_t M, const __nv_bfloat16* ut, float* dx, int dx_acc,
                    __nv_bfloat16* dx_bf, std::string& err) {
   LinearBwd b;
   b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;
+  b.dz_ready = dy == nullptr;
   b.ut = ut; b.ut_ld = m.ut_ld; b.dx = dx; b.dx_accumulate = dx_acc; b.dx_bf = dx_bf;
   if (t) {
     b.dA = m.g + t->offA; b.dB = m.g + t->offB; b.dm = t->offM >= 0 ? m.g + t->offM : nullptr;
@@ -386,10 +388,15 @@ static int dit_step(DitModel& m, std::string& err) {
     DitTarget *tp = target(m, m.bname(l, "ff.proj.weight")), *tf = target(m, m.bname(l, "ff.out.weight"));
     const long ms = 6L * D;
     // feed-forward branch
-    if (k_gate_bwd(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, m.dtmp, err)) return 1;
-    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, m.dtmp, M, a.ut[3], m.dact, 0, nullptr, err)) return 1;
-    if (k_swiglu_bwd(c, m.dact, a.ff, (int)M, I, m.dtmp, err)) return 1;
-    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, m.dtmp, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
+    // (the gate and SwiGLU backward write the adapted linears' dz / dg directly)
+    if (k_gate_bwd_dz(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, a.yf, b_fo, tf && tf->prep.dora() ? tf->prep.g : nullptr,
+                      m.dz, m.dg, err))
+      return 1;
+    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, a.ut[3], m.dact, 0, nullptr, err)) return 1;
+    if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, m.dz, m.dg,
+                        err))
+      return 1;
+    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, err)) return 1;
     // cross-attention branch (context and its projections are frozen: only dq flows)
     if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, m.gx, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
@@ -412,8 +419,10 @@ static int dit_step(DitModel& m, std::string& err) {
     if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, m.dh, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, err)) return 1;
     // self-attention branch
-    if (k_gate_bwd(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, m.dtmp, err)) return 1;
-    if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, m.dtmp, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
+    if (k_gate_bwd_dz(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, a.yo, nullptr,
+                      to && to->prep.dora() ? to->prep.g : nullptr, m.dz, m.dg, err))
+      return 1;
+    if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, nullptr, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
     {
       AttnArgs sa;
       sa.B = B; sa.H = H; sa.Sq = S; sa.Sk = S; sa.scale = scale; sa.window = -1;

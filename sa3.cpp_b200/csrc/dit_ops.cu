@@ -112,18 +112,18 @@ struct HeadSlices {
   int n;
 };
 
+// Grid (ceil(H * nslices / 8), rows): block y = token row t (strided past 65535), warp w of the
+// block = (slice, head) pair blockIdx.x * 8 + w.
 __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
                                      int tps, float eps, int rot, const float2* __restrict__ tab,
                                      __nv_bfloat16* __restrict__ out) {
   const int nslices = slices.n;
-  const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const long total = (long)T * H * nslices;
-  if (wid >= total) return;
+  const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pair >= H * nslices) return;
   const int lane = threadIdx.x & 31;
-  const int si = (int)(wid % nslices);
-  const int h = (int)((wid / nslices) % H);
-  const int t = (int)(wid / ((long)nslices * H));
+  const int si = pair % nslices, h = pair / nslices;
   const HeadSlice sl = slices.s[si];
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
   const long base = (long)t * ncols + sl.col + h * 64;
   float a = y[base + lane], b = y[base + lane + 32];
   if (sl.gamma) {
@@ -149,15 +149,16 @@ __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int nco
   }
   out[base + lane] = __float2bfloat16_rn(a);
   out[base + lane + 32] = __float2bfloat16_rn(b);
+  }
 }
 
 __global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, const float* __restrict__ y, int T,
                                      int ncols, int H, HeadSlice sl, int tps, int rot,
                                      const float2* __restrict__ tab, float* __restrict__ dy) {
-  const long wid = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (wid >= (long)T * H) return;
+  const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (h >= H) return;
   const int lane = threadIdx.x & 31;
-  const int h = (int)(wid % H), t = (int)(wid / H);
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
   float ga = g[(long)t * g_ld + h * 64 + lane], gb = g[(long)t * g_ld + h * 64 + lane + 32];
   const long base = (long)t * ncols + sl.col + h * 64;
   if (sl.rope) {   // inverse rotation of the gradient
@@ -185,31 +186,34 @@ __global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, con
   }
   dy[base + lane] = ga;
   dy[base + lane + 32] = gb;
+  }
 }
 
+// Grid (ceil(D / 4 / 256), rows): thread = 4 consecutive columns of one row.
 __global__ void gate_residual_kernel(const float* __restrict__ x_in, const float* __restrict__ y,
                                      const float* __restrict__ gate, long gstride, int T, int D, int tps,
                                      float* __restrict__ x_out) {
-  const long n4 = (long)T * D / 4;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
-    const long e = i * 4;
-    const int t = (int)(e / D), cidx = (int)(e % D);
+  const int cidx = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (cidx >= D) return;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+    const long e = (long)t * D + cidx;
     const float4 gv = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + cidx);
-    const float4 a = reinterpret_cast<const float4*>(x_in)[i];
-    const float4 b = reinterpret_cast<const float4*>(y)[i];
-    reinterpret_cast<float4*>(x_out)[i] = make_float4(a.x + b.x * gv.x, a.y + b.y * gv.y, a.z + b.z * gv.z, a.w + b.w * gv.w);
+    const float4 a = *reinterpret_cast<const float4*>(x_in + e);
+    const float4 b = *reinterpret_cast<const float4*>(y + e);
+    *reinterpret_cast<float4*>(x_out + e) =
+        make_float4(a.x + b.x * gv.x, a.y + b.y * gv.y, a.z + b.z * gv.z, a.w + b.w * gv.w);
   }
 }
 
 __global__ void gate_bwd_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride, int T,
                                 int D, int tps, float* __restrict__ dy) {
-  const long n4 = (long)T * D / 4;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
-    const long e = i * 4;
-    const int t = (int)(e / D), cidx = (int)(e % D);
+  const int cidx = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (cidx >= D) return;
+  for (int t = blockIdx.y; t < T; t += gridDim.y) {
+    const long e = (long)t * D + cidx;
     const float4 gv = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + cidx);
-    const float4 a = reinterpret_cast<const float4*>(gx)[i];
-    reinterpret_cast<float4*>(dy)[i] = make_float4(a.x * gv.x, a.y * gv.y, a.z * gv.z, a.w * gv.w);
+    const float4 a = *reinterpret_cast<const float4*>(gx + e);
+    *reinterpret_cast<float4*>(dy + e) = make_float4(a.x * gv.x, a.y * gv.y, a.z * gv.z, a.w * gv.w);
   }
 }
 
@@ -371,8 +375,8 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   const float2* tab = nullptr;
   if (any_rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
-  const long warps = (long)T * H * nslices;
-  head_prep_fwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot, tab, out);
+  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)(T < 65535 ? T : 65535));
+  head_prep_fwd_kernel<<<grid, 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
 
@@ -381,22 +385,25 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
-  const long warps = (long)T * H;
-  head_prep_bwd_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
+  const dim3 grid((unsigned)((H + 7) / 8), (unsigned)(T < 65535 ? T : 65535));
+  head_prep_bwd_kernel<<<grid, 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
   return check_launch("head_prep_bwd", err);
 }
 
 int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate, long gstride, int T, int D, int tps,
                     float* x_out, std::string& err) {
   ProfScope prof_(c, "gate_residual");
-  gate_residual_kernel<<<gs((long)T * D / 4), 256, 0, c->stream>>>(x_in, y, gate, gstride, T, D, tps, x_out);
+  if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
+  gate_residual_kernel<<<dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0,
+                         c->stream>>>(x_in, y, gate, gstride, T, D, tps, x_out);
   return check_launch("gate_residual", err);
 }
 
 int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, float* dy,
                std::string& err) {
   ProfScope prof_(c, "gate_bwd");
-  gate_bwd_kernel<<<gs((long)T * D / 4), 256, 0, c->stream>>>(gx, gate, gstride, T, D, tps, dy);
+  if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
+  gate_bwd_kernel<<<dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(gx, gate, gstride, T, D, tps, dy);
   return check_launch("gate_bwd", err);
 }
 

@@ -96,11 +96,13 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
   const bool dora = ad && ad->dora();
   const int64_t in = w->in, out = w->out;
   const int rank = ad ? ad->rank : 0;
-  if (dora && cudaMemsetAsync(b.dg, 0, sizeof(float) * out, c->stream) != cudaSuccess)
-    return check_launch("memset", err);
-  if (k_bwd_prologue(c, b.dy, dora ? b.y : nullptr, b.bias, dora ? ad->g : nullptr, b.M, out, b.dz,
-                     dora ? b.dg : nullptr, err))
-    return 1;
+  if (!b.dz_ready) {
+    if (dora && cudaMemsetAsync(b.dg, 0, sizeof(float) * out, c->stream) != cudaSuccess)
+      return check_launch("memset", err);
+    if (k_bwd_prologue(c, b.dy, dora ? b.y : nullptr, b.bias, dora ? ad->g : nullptr, b.M, out, b.dz,
+                       dora ? b.dg : nullptr, err))
+      return 1;
+  }
   if (ad) {
     GemmDesc g;   // du = s dz B  [M][16]
     g.M = (int)b.M; g.N = 16; g.K = (int)out;

@@ -134,6 +134,116 @@ __global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __re
   g[o] = m[o] / sqrtf(n2);
 }
 
+// ---------------------------------------------------------------- producers fused with the prologue
+// The upstream gradient dy of an adapted linear is produced here and never stored in f32: the
+// kernels write dz = bf16(g * dy) (bf16(dy) without DoRA) and add colsum(dy * z) into dg, with
+// z = (y - bias) / g the pre-scale output of the forward.  Thread = 4 columns, block = kFuseTok
+// rows (one f32 atomic per column and block).
+constexpr int kFuseTok = 32;
+
+__device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4], const float (&gv)[4], bool dora) {
+  uint2 pk;
+  pk.x = pack_bf16x2(dora ? dy[0] * gv[0] : dy[0], dora ? dy[1] * gv[1] : dy[1]);
+  pk.y = pack_bf16x2(dora ? dy[2] * gv[2] : dy[2], dora ? dy[3] * gv[3] : dy[3]);
+  *reinterpret_cast<uint2*>(dz) = pk;
+}
+
+// dy = gx * gate[sample] (the gate backward of src/dit.h:186-193)
+__global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride,
+                                   int T, int D, int tps, const float* __restrict__ y, const float* __restrict__ bias,
+                                   const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
+                                   float* __restrict__ dg) {
+  const int c0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c0 >= D) return;
+  const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
+  const bool dora = g != nullptr;
+  float gv[4] = {1.f, 1.f, 1.f, 1.f}, inv[4] = {1.f, 1.f, 1.f, 1.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (dora) {
+    const float4 g4 = *reinterpret_cast<const float4*>(g + c0);
+    gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) inv[e] = 1.f / gv[e];
+    if (bias) {
+      const float4 b4 = *reinterpret_cast<const float4*>(bias + c0);
+      bv[0] = b4.x; bv[1] = b4.y; bv[2] = b4.z; bv[3] = b4.w;
+    }
+  }
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = t0; t < t1; ++t) {
+    const long e = (long)t * D + c0;
+    const float4 gt = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + c0);
+    const float4 a = *reinterpret_cast<const float4*>(gx + e);
+    const float dy[4] = {a.x * gt.x, a.y * gt.y, a.z * gt.z, a.w * gt.w};
+    dz_store4(dz + e, dy, gv, dora);
+    if (dora) {
+      const float4 yv = *reinterpret_cast<const float4*>(y + e);
+      acc[0] = fmaf(dy[0], (yv.x - bv[0]) * inv[0], acc[0]);
+      acc[1] = fmaf(dy[1], (yv.y - bv[1]) * inv[1], acc[1]);
+      acc[2] = fmaf(dy[2], (yv.z - bv[2]) * inv[2], acc[2]);
+      acc[3] = fmaf(dy[3], (yv.w - bv[3]) * inv[3], acc[3]);
+    }
+  }
+  if (dora) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) atomicAdd(dg + c0 + q, acc[q]);
+  }
+}
+
+// SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output, da the gradient
+// of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I columns).
+__global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
+                                     const float* __restrict__ bias, const float* __restrict__ g,
+                                     __nv_bfloat16* __restrict__ dz, float* __restrict__ dg) {
+  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (j >= I) return;
+  const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
+  const bool dora = g != nullptr;
+  float gvv[4] = {1.f, 1.f, 1.f, 1.f}, ggg[4] = {1.f, 1.f, 1.f, 1.f};
+  float bvv[4] = {0.f, 0.f, 0.f, 0.f}, bgg[4] = {0.f, 0.f, 0.f, 0.f};
+  if (dora) {
+    const float4 a4 = *reinterpret_cast<const float4*>(g + j), b4 = *reinterpret_cast<const float4*>(g + I + j);
+    gvv[0] = a4.x; gvv[1] = a4.y; gvv[2] = a4.z; gvv[3] = a4.w;
+    ggg[0] = b4.x; ggg[1] = b4.y; ggg[2] = b4.z; ggg[3] = b4.w;
+    if (bias) {
+      const float4 c4 = *reinterpret_cast<const float4*>(bias + j), d4 = *reinterpret_cast<const float4*>(bias + I + j);
+      bvv[0] = c4.x; bvv[1] = c4.y; bvv[2] = c4.z; bvv[3] = c4.w;
+      bgg[0] = d4.x; bgg[1] = d4.y; bgg[2] = d4.z; bgg[3] = d4.w;
+    }
+  }
+  float accv[4] = {0.f, 0.f, 0.f, 0.f}, accg[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int t = t0; t < t1; ++t) {
+    const float* fr = f + (long)t * 2 * I;
+    const float4 v = *reinterpret_cast<const float4*>(fr + j);
+    const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
+    const float4 d = *reinterpret_cast<const float4*>(da + (long)t * I + j);
+    const float vv[4] = {v.x, v.y, v.z, v.w}, gg[4] = {gl.x, gl.y, gl.z, gl.w}, dd[4] = {d.x, d.y, d.z, d.w};
+    float dv[4], dgl[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float sg = 1.f / (1.f + __expf(-gg[e]));
+      dv[e] = dd[e] * gg[e] * sg;
+      dgl[e] = dd[e] * vv[e] * sg * (1.f + gg[e] * (1.f - sg));
+    }
+    __nv_bfloat16* zr = dz + (long)t * 2 * I;
+    dz_store4(zr + j, dv, gvv, dora);
+    dz_store4(zr + I + j, dgl, ggg, dora);
+    if (dora) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        accv[e] = fmaf(dv[e], (vv[e] - bvv[e]) / gvv[e], accv[e]);
+        accg[e] = fmaf(dgl[e], (gg[e] - bgg[e]) / ggg[e], accg[e]);
+      }
+    }
+  }
+  if (dora) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      atomicAdd(dg + j + e, accv[e]);
+      atomicAdd(dg + I + j + e, accg[e]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- grouped adapter preparation
 // The same three preparations for every adapter of a model in one launch each (grid.y = adapter),
 // driven by a device array of PrepDesc built once when the adapters are bound.
@@ -372,6 +482,28 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
   dora_bwd_kernel<<<(unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, c->stream>>>(
       pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_acc, dB, cb, c3);
   return check_launch("dora_bwd", err);
+}
+
+int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
+                  const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
+  if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
+  if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "gate: too many rows"; return 1; }
+  if (g && cudaMemsetAsync(dg, 0, sizeof(float) * D, c->stream) != cudaSuccess) return check_launch("memset", err);
+  ProfScope prof_(c, "gate_bwd_dz");
+  gate_bwd_dz_kernel<<<dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0,
+                       c->stream>>>(gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
+  return check_launch("gate_bwd_dz", err);
+}
+
+int k_swiglu_bwd_dz(Ctx* c, const float* da, const float* f, int T, int I, const float* bias, const float* g,
+                    __nv_bfloat16* dz, float* dg, std::string& err) {
+  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
+  if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }
+  if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 2 * I, c->stream) != cudaSuccess) return check_launch("memset", err);
+  ProfScope prof_(c, "swiglu_bwd_dz");
+  swiglu_bwd_dz_kernel<<<dim3((unsigned)((I / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0,
+                         c->stream>>>(da, f, T, I, bias, g, dz, dg);
+  return check_launch("swiglu_bwd_dz", err);
 }
 
 int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {

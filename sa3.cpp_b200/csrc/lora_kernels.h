@@ -31,6 +31,12 @@ int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in,
 int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err);
 int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                 const float* bns, const float* m, float s, float* nsq, float* g, std::string& err);
+// Producers of an adapted linear's output gradient fused with its backward prologue: write
+// dz = bf16(g * dy) and dg = colsum(dy * (y - bias) / g) (dg zeroed first; g null: dz = bf16(dy)).
+int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
+                  const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err);
+int k_swiglu_bwd_dz(Ctx* c, const float* da, const float* f, int T, int I, const float* bias, const float* g,
+                    __nv_bfloat16* dz, float* dg, std::string& err);
 int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
                    int64_t out, __nv_bfloat16* dz, float* dg, std::string& err);
 int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
