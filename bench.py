@@ -286,6 +286,14 @@ def main_linear(args):
 
     for _ in range(3):
         graph_step()
+    if args.profile_step:
+        # one replay between cudaProfilerStart / Stop: `ncu --profile-from-start off` sees exactly
+        # the launches of one step
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        graph_step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     ctx.profile_enable(timing=0)
     with Clocks(local) as clk:
         total_ms = timed(graph_step, args.steps)
@@ -646,6 +654,14 @@ def main_dit(args):
 
     for _ in range(3):
         graph_step()
+    if args.profile_step:
+        # one replay between cudaProfilerStart / Stop: `ncu --profile-from-start off` sees exactly
+        # the launches of one step
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        graph_step()
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     ctx.profile_enable(timing=0)
     with Clocks(local) as clk:
         total_ms = timed(graph_step, args.steps)
@@ -830,6 +846,8 @@ def main():
     ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
     ap.add_argument("--workload", default="dit", choices=["dit", "linear", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="dit: bracket one extra graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.workload == "linear":

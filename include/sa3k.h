@@ -60,8 +60,9 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       model; 128, 192 or 256 fixes it (a tuning knob; results do not depend on it). */
 #define SA3K_OPT_GEMM_TILE_N 3
 /* SA3K_OPT_GEMM_PAIR  1 (default): bf16-operand GEMMs with at least 256 rows and enough output
- *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always.
- *       Results are identical either way (same per-element summation order). */
+ *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always;
+ *       2: CTA pairs wherever they apply (a tuning knob; with SA3K_OPT_GEMM_TILE_N 192 the pair
+ *       tiles are 256 x 192).  Results are identical either way (same per-element summation order). */
 #define SA3K_OPT_GEMM_PAIR 4
 /* SA3K_OPT_ATTN_TC  1 (default): attention on the tcgen05 tensor cores (TMEM accumulators, P and
  *       dS fed back from TMEM); 0: the mma.sync kernels.  Both compute in bf16 with f32

@@ -45,7 +45,7 @@ void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err) {
 
 // Scratch slots of the C-ABI linear entry points.
 enum Slot : int {
-  kS_XBF = 0, kS_PREP, kS_U, kS_EXTU, kS_UT, kS_DZ, kS_DG, kS_DU, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_HOST_IO, kS_OPT,
+  kS_XBF = 0, kS_PREP, kS_EXTU, kS_UT, kS_DZ, kS_DG, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_HOST_IO, kS_OPT,
   kS_COUNT
 };
 
@@ -78,7 +78,6 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (k_cvt_bf16(c, x, S * in, x_bf, err)) return 1;
 
   AdapterPrep prep;
-  float *u = nullptr;
   __nv_bfloat16 *ext_u = nullptr, *ut = nullptr;
   if (adapter) {
     prep.rank = ad->rank; prep.in = in; prep.out = out; prep.s = ad->scale;
@@ -87,24 +86,17 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     if (!mem) return 1;
     adapter_bind(prep, mem);
     if (adapter_prepare(c, w, prep, err)) return 1;
-    if (!get(c, kS_U, S * 16, u, err) || !get(c, kS_EXTU, S * 64, ext_u, err) || !get(c, kS_UT, 16 * s_pad, ut, err))
+    if (!get(c, kS_EXTU, S * 64, ext_u, err) || !get(c, kS_UT, 16 * s_pad, ut, err))
       return 1;
   }
   if (fwd || (bwd && adapter)) {
     // the backward needs u^T, which the forward produces; a backward-only call recomputes it
     LinearFwd f;
     f.w = w; f.ad = adapter ? &prep : nullptr; f.bias = bias; f.x_bf = x_bf; f.M = S;
-    f.y = y_out; f.u = u; f.ext_u = ext_u; f.ut = ut; f.ut_ld = s_pad;
+    f.y = y_out; f.ext_u = ext_u; f.ut = ut; f.ut_ld = s_pad;
     if (!fwd) {
-      // u only: run the rank-16 GEMM and pack (the main GEMM is skipped without an output)
-      GemmDesc g;
-      g.M = (int)S; g.N = 16; g.K = (int)in;
-      g.a = x_bf; g.lda = in;
-      g.bsrc = kB_BF16_KMAJOR; g.b = prep.a_bf; g.ldb = in;
-      g.out = u; g.ldo = 16; g.bn = 16;
-      g.name = "lora.u";
-      if (gemm(c, g, err)) return 1;
-      if (k_pack_rank(c, u, (int)S, prep.s, ext_u, 1.0f, ut, (int)s_pad, err)) return 1;
+      // u only (the main GEMM is skipped without an output)
+      if (lora_u(c, x_bf, S, in, prep, ext_u, ut, s_pad, err)) return 1;
     } else if (linear_forward(c, f, err)) {
       return 1;
     }
@@ -118,7 +110,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (!get(c, kS_DZ, S * out, b.dz, err)) return 1;
   if (dora && (!get(c, kS_DG, out, b.dg, err) || !get(c, kS_CB, 16 * out, b.cb, err) || !get(c, kS_C3, 256, b.c3, err)))
     return 1;
-  if (adapter && (!get(c, kS_DU, S * 16, b.du, err) || !get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
+  if (adapter && (!get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
                   !get(c, kS_DUT, 16 * s_pad, b.dut, err)))
     return 1;
   return linear_backward(c, b, err);
@@ -260,7 +252,10 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
         return fill_err(err, err_len, "tile N must be 0, 128, 192 or 256");
       ctx->c.tile_n = (int)value;
       return 0;
-    case SA3K_OPT_GEMM_PAIR: ctx->c.gemm_pair = value != 0; return 0;
+    case SA3K_OPT_GEMM_PAIR:
+      if (value < 0 || value > 2) return fill_err(err, err_len, "GEMM pair option must be 0, 1 or 2");
+      ctx->c.gemm_pair = (int)value;
+      return 0;
     case SA3K_OPT_ATTN_TC: ctx->c.attn_tc = value != 0; return 0;
     default: return fill_err(err, err_len, "unknown option");
   }

@@ -162,33 +162,6 @@ struct Waiter {
   }
 };
 
-// Warp-wide bounded wait: every lane of the warp calls it and all get the same answer (the
-// warp stays converged for the .aligned tcgen05 instructions that follow).
-struct WaiterW {
-  volatile int* abort_flag;
-  int* err;
-  __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity, int code) const {
-    const uint32_t a = smem_u32(bar);
-    if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;   // fast path: already complete
-    if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t i = 0;; ++i) {
-      if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
-      if ((i & 63u) == 63u) {
-        if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
-        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitLimitNs)) {
-          if ((threadIdx.x & 31) == 0) {
-            record_error(err, code);
-            *abort_flag = 1;
-          }
-          __syncwarp();
-          return false;
-        }
-      }
-    }
-  }
-};
-
 __device__ __forceinline__ bool visible(int qi, int kj, int Sk, int window) {
   return kj < Sk && (window < 0 || abs(qi - kj) <= window);
 }
@@ -286,7 +259,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
-  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
+  const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -557,7 +530,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
-  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
+  const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -853,7 +826,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   const uint32_t tbase = *tmem_slot;
   const uint32_t tV = tbase + 384, tK = tbase + 448;
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
-  const WaiterW waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
+  const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
   if (warp == 0) {
     if (lane == 0) {

@@ -49,6 +49,24 @@ static int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, ui
   return 0;
 }
 
+// Per-tile split counters of the split-K GEMMs (split-K runs only with at most sm_count / 2
+// output tiles).  Zeroed once when allocated; the kernel resets each counter it completes.
+static int* split_counters(Ctx* c, std::string& err) {
+  constexpr size_t kCounters = 1024;
+  const bool fresh = (int)c->scratch.size() <= kSlotSplitCnt || !c->scratch[(size_t)kSlotSplitCnt].ptr;
+  int* p = static_cast<int*>(scratch_get(c, kSlotSplitCnt, kCounters * sizeof(int), err));
+  if (!p) return nullptr;
+  if (fresh && cudaMemsetAsync(p, 0, kCounters * sizeof(int), c->stream) != cudaSuccess) {
+    check_launch("split counters", err);
+    return nullptr;
+  }
+  if ((size_t)c->sm_count / 2 > kCounters) {
+    err = "gemm: too many SMs for the split-K counters";
+    return nullptr;
+  }
+  return p;
+}
+
 template <int BN, int STAGES, int BMODE, bool A_MN>
 static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tbs, const CUtensorMap& tea, const CUtensorMap& teb,
@@ -91,6 +109,8 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
         float* part = static_cast<float*>(scratch_get(c, kSlotSplitK, (size_t)splits * d.M * d.N * sizeof(float), err));
         if (!part) return 1;
         a.partial = part;
+        a.tile_cnt = split_counters(c, err);
+        if (!a.tile_cnt) return 1;
       }
     }
   }
@@ -99,11 +119,11 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   a.tma_out = 0;
   if (a.splits == 1) {
     std::string e2;
-    if (d.out && !d.out_bf && !d.out_trans && (d.ldo % 4) == 0 &&
+    if (d.out && !d.out_bf && !d.out_bf_t && !d.out_trans && (d.ldo % 4) == 0 &&
         (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
         !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d.out, d.N, d.M, d.ldo * 4, 32, 32, SW, "out", e2))
       a.tma_out = 1;
-    else if (d.out_bf && !d.out && !d.out_bf_trans && BN >= 64 && (d.ldo_bf % 8) == 0 &&
+    else if (d.out_bf && !d.out && !d.out_bf_trans && !d.out_bf_t && d.bf_scale == 1.0f && BN >= 64 && (d.ldo_bf % 8) == 0 &&
              (reinterpret_cast<uintptr_t>(d.out_bf) & 15) == 0 &&
              !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
       a.tma_out = 2;
@@ -114,14 +134,6 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
     ProfScope prof_(c, d.name);
     kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, tout, a);
     if (check_launch("gemm_tc", err)) return 1;
-  }
-  if (a.splits > 1 && !a.atomic) {
-    ProfScope prof_(c, "splitk_reduce");
-    const long mn = (long)d.M * d.N;
-    long blocks = (mn + 255) / 256;
-    if (blocks > 148 * 8) blocks = 148 * 8;
-    splitk_reduce_kernel<<<(unsigned)blocks, 256, 0, c->stream>>>(a);
-    return check_launch("splitk_reduce", err);
   }
   return 0;
 }
@@ -142,7 +154,7 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
     at[0].id = cudaLaunchAttributeClusterDimension;
     at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
     q.gridDim = dim3(2 * (unsigned)(c->sm_count / 2));
-    q.blockDim = dim3(192);
+    q.blockDim = dim3(kPairThreads);
     q.dynamicSmemBytes = L::DYN;
     q.attrs = at;
     q.numAttrs = 1;
@@ -176,7 +188,7 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
   cfg.gridDim = dim3((unsigned)(2 * clusters));
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kPairThreads);
   cfg.dynamicSmemBytes = L::DYN;
   cfg.stream = c->stream;
   cfg.attrs = at;
@@ -296,7 +308,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.has_ext = d.ext_a ? 1 : 0;
   a.col_scale = d.col_scale; a.col_bias = d.col_bias; a.alpha = d.alpha;
   a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
-  a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans;
+  a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans; a.bf_scale = d.bf_scale;
+  a.out_bf_t = d.out_bf_t; a.ldo_bf_t = d.ldo_bf_t;
+  a.tile_cnt = nullptr;
   a.err = c->d_err;
   a.splits = 1;
   a.kb_per_split = 1;
@@ -310,13 +324,26 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
                   : launch<16, 8, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
   }
   if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
-  // CTA pairs for the bf16-operand GEMMs with enough output tiles to fill the GPU without split-K
-  // (measured: pairs win once every cluster gets many 256 x 256 tiles; with few tiles per
-  // cluster the one-CTA kernel with its better-balanced waves is faster)
-  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM && d.N >= 256 && c->tile_n != 128 && c->tile_n != 192) {
-    const long ptiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + 255) / 256);
-    if (ptiles >= 8L * (c->sm_count / 2)) {
-      const int bp = 256;
+  // CTA pairs for the bf16-operand GEMMs with at least one full round of pair tiles (measured on
+  // the DiT shapes: pairs match or beat the one-CTA kernel from there on; half the B bytes per
+  // SM per MMA cycle).  The pair N tile (256, or 192 for K-major B) minimises rounds x tile
+  // width / efficiency, 256 x 192 pair tiles running at about 0.85 of 256 x 256 per column.
+  // gemm_pair 2 forces pairs wherever they apply (tile_n 192 picks 256 x 192 pair tiles).
+  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM && d.N >= 256 && !d.out_bf_t && d.bf_scale == 1.0f) {
+    int bp = 0;
+    if (c->gemm_pair == 2) {
+      bp = (c->tile_n == 192 && bmode == 0) ? 192 : 256;
+    } else if (c->tile_n == 0) {
+      const long clusters = (long)(c->sm_count / 2);
+      const long tm2 = (d.M + 2 * kBM - 1) / (2 * kBM);
+      const long t256 = tm2 * ((d.N + 255) / 256), t192 = tm2 * ((d.N + 191) / 192);
+      if (t256 >= clusters) {
+        const double c256 = (double)((t256 + clusters - 1) / clusters) * 256.0;
+        const double c192 = (double)((t192 + clusters - 1) / clusters) * 192.0 / 0.85;
+        bp = (bmode == 0 && c192 < c256) ? 192 : 256;
+      }
+    }
+    if (bp) {
       CUtensorMap tb2 = tb, tea2 = tea, teb2 = teb;
       // B halves: BN/2 rows (K-major) per CTA; MN-major B keeps its 64-wide atoms
       if (bmode == 0) {
@@ -328,6 +355,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       if (d.ext_a) {
         if (make_map(&teb2, BF, d.ext_b, 64, d.N, 128, 64, bp / 2, SW, "ext B half", err)) return 1;
       }
+      if (bp == 192) return launch_pair<192, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err);
       return bmode == 0 ? launch_pair<256, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err)
                         : launch_pair<256, 6, 1>(c, d, ta, tb2, tea2, teb2, a, err);
     }

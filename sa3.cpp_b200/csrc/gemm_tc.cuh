@@ -7,7 +7,7 @@
 // 128 x BN output tile with a warp-specialized pipeline:
 //
 //   warp 0      TMA producer: A tile (bf16) + B tile (bf16) or the raw quantized B bytes + scales
-//   warp 1      TMEM allocator and the single MMA-issuing thread (tcgen05.mma kind::f16)
+//   warp 1      TMEM allocator and MMA issue (tcgen05.mma kind::f16, one elected lane)
 //   warps 2-5   dequant stage (quantized B only): raw bytes -> bf16 in the 128B-swizzled UMMA
 //               layout, then the epilogue: tcgen05.ld of the accumulator -> scale/bias -> global
 //
@@ -43,12 +43,17 @@ struct GemmArgs {
   long ldo;                 // its leading dimension (elements)
   int out_trans;            // 0: out[m*ldo + n]; 1: out[n*ldo + m]
   int accumulate;           // add into out instead of overwriting
-  __nv_bfloat16* out_bf;    // bf16 output (nullable), same scale/bias as out
+  __nv_bfloat16* out_bf;    // bf16 output (nullable): bf_scale * the value written to out
   long ldo_bf;
   int out_bf_trans;
+  float bf_scale;
+  __nv_bfloat16* out_bf_t;  // second bf16 output, transposed: out_bf_t[n * ldo_bf_t + m] (nullable)
+  long ldo_bf_t;
   int splits;               // split-K: work item = (tile, split); 1 = no split
   int kb_per_split;         // 64-wide k-blocks per split
-  float* partial;           // split-K: raw f32 partial sums [splits][M][N] (epilogue deferred)
+  float* partial;           // split-K: raw f32 partial sums [splits][M][N]; the CTA that finishes a
+                            //   tile's last split sums them in split order and runs the epilogue
+  int* tile_cnt;            // split-K: per-tile count of finished splits (zero between launches)
   int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: bf16 `out_bf` via TMA
                             //    store; 0: direct stores (split-K partials, transposed or dual outputs)
   int atomic;               // split-K: every split adds its (scaled) part into `out` with atomics
@@ -67,10 +72,12 @@ struct BModeTraits {
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2..5 epilogue, 6.. dequant (quant only).
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, then the epilogue warps (8 for bf16
+// operands: two per TMEM lane quarter, splitting the accumulator columns; 4 with the dequant
+// stage), then the dequant warps (quantized B only).
 template <int BMODE>
 struct GemmRoles {
-  static constexpr int EPI_WARPS = 4;
+  static constexpr int EPI_WARPS = BModeTraits<BMODE>::quant ? 4 : 8;
   static constexpr int DQ_WARPS = BModeTraits<BMODE>::quant ? 8 : 0;
   static constexpr int THREADS = 32 * (2 + EPI_WARPS + DQ_WARPS);
   static constexpr int DQ_THREADS = 32 * DQ_WARPS;
@@ -78,6 +85,7 @@ struct GemmRoles {
 
 template <int BN, int STAGES, int BMODE>
 struct GemmSmem {
+  static constexpr int EPI_WARPS = GemmRoles<BMODE>::EPI_WARPS;
   static constexpr int A_BYTES = kBM * kBK * 2;
   static constexpr int B_BYTES = BN * kBK * 2;
   static constexpr int RAW_BYTES =
@@ -90,13 +98,14 @@ struct GemmSmem {
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_RAW = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_STRIDE;
-  // epilogue: two 4 KB staging buffers per epilogue warp (32 rows x 128 B, 128B-swizzled), the
+  // epilogue: 4 KB staging buffers per epilogue warp (32 rows x 128 B, 128B-swizzled), the
   // source of the TMA stores (or of the coalescing transpose on the direct path)
   static constexpr int OFF_STAGE = align_up(OFF_SC + STAGES * SC_STRIDE, 1024);
   static constexpr int STAGE_BYTES = 4096;
   // two staging buffers per warp when they fit next to the pipeline stages, else one
-  static constexpr int STAGE_BUFS = (OFF_STAGE + 4 * 2 * STAGE_BYTES + 1024 + 256 <= 232448) ? 2 : 1;
-  static constexpr int OFF_BAR = OFF_STAGE + 4 * STAGE_BUFS * STAGE_BYTES;
+  static constexpr int STAGE_BUFS =
+      (OFF_STAGE + EPI_WARPS * 2 * STAGE_BYTES + (3 * STAGES + 4) * 8 + 16 + 1024 <= 232448) ? 2 : 1;
+  static constexpr int OFF_BAR = OFF_STAGE + EPI_WARPS * STAGE_BUFS * STAGE_BYTES;
   static constexpr int BAR_BYTES = (3 * STAGES + 4) * 8 + 16;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
   static constexpr int DYN = TOTAL + 1024;   // slack for 1024-byte alignment of the base
@@ -176,29 +185,6 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* raw, const uint8_t*
   }
 }
 
-// ------------------------------------------------------------------ split-K reduction
-// out = epilogue(alpha * sum_s partial[s]) with the same column scale / bias / accumulate /
-// transpose / bf16 options as the GEMM epilogue.  Deterministic (fixed summation order).
-__global__ void splitk_reduce_kernel(const GemmArgs args) {
-  const long mn = (long)args.M * args.N;
-  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < mn; i += (long)gridDim.x * blockDim.x) {
-    const int m = (int)(i / args.N), n = (int)(i % args.N);
-    float x = 0.f;
-    for (int sp = 0; sp < args.splits; ++sp) x += args.partial[(long)sp * mn + i];
-    x *= args.alpha;
-    if (args.col_scale) x *= args.col_scale[n];
-    if (args.col_bias) x += args.col_bias[n];
-    if (args.out) {
-      float* dst = args.out_trans ? args.out + (long)n * args.ldo + m : args.out + (long)m * args.ldo + n;
-      *dst = args.accumulate ? *dst + x : x;
-    }
-    if (args.out_bf) {
-      __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)n * args.ldo_bf + m : args.out_bf + (long)m * args.ldo_bf + n;
-      *dst = __float2bfloat16_rn(x);
-    }
-  }
-}
-
 // ------------------------------------------------------------------ epilogue arithmetic
 // f[j] = acc[j] * (alpha * col_scale[n0 + j]) + col_bias[n0 + j] for 32 accumulator columns
 // (raw sums for split-K partials).  Column vectors are read 4 at a time (the same addresses for
@@ -230,6 +216,54 @@ __device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, i
         if (col_bias) cb = col_bias[n];
       }
       f[j] = __uint_as_float(v[j]) * cs + cb;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ split-K completion
+// The tile [m0, m0 + rows) x [n0, n0 + cols) of out = epilogue(alpha * sum_s partial[s]), summed in
+// split order (deterministic) by the nt threads tid = 0 .. nt-1.  Partials are read from L2
+// (__ldcg: other CTAs wrote them).  Four columns per thread when N % 4 == 0 (n0 is a multiple of
+// the N tile); the mapping is column-fastest for row-major outputs (coalesced partial reads and
+// output writes) and row-fastest when an output is transposed.
+__device__ __forceinline__ void splitk_finish(const GemmArgs& args, int m0, int n0, int rows, int cols, int tid,
+                                              int nt) {
+  const long mn = (long)args.M * args.N;
+  const bool trans = args.out_trans || args.out_bf_trans || args.out_bf_t;
+  const int vw = (args.N % 4 == 0) ? 4 : 1;
+  const int cg = (cols + vw - 1) / vw;
+  for (int e = tid; e < rows * cg; e += nt) {
+    const int r = trans ? e % rows : e / cg, cq = trans ? e / rows : e % cg;
+    const int row = m0 + r, col0 = n0 + vw * cq;
+    const float* src = args.partial + (long)row * args.N + col0;
+    float x[4] = {0.f, 0.f, 0.f, 0.f};
+    if (vw == 4) {
+#pragma unroll 4
+      for (int sp = 0; sp < args.splits; ++sp) {
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(src + sp * mn));
+        x[0] += p.x; x[1] += p.y; x[2] += p.z; x[3] += p.w;
+      }
+    } else {
+#pragma unroll 4
+      for (int sp = 0; sp < args.splits; ++sp) x[0] += __ldcg(src + sp * mn);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int col = col0 + u;
+      if (u >= vw || col >= n0 + cols) break;
+      float v = x[u] * args.alpha;
+      if (args.col_scale) v *= args.col_scale[col];
+      if (args.col_bias) v += args.col_bias[col];
+      if (args.out) {
+        float* dst = args.out_trans ? args.out + (long)col * args.ldo + row : args.out + (long)row * args.ldo + col;
+        *dst = args.accumulate ? *dst + v : v;
+      }
+      if (args.out_bf) {
+        __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)col * args.ldo_bf + row
+                                               : args.out_bf + (long)row * args.ldo_bf + col;
+        *dst = __float2bfloat16_rn(v * args.bf_scale);
+      }
+      if (args.out_bf_t) args.out_bf_t[(long)col * args.ldo_bf_t + row] = __float2bfloat16_rn(v);
     }
   }
 }
@@ -377,56 +411,65 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
-      const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
-      int it = 0, ti = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++ti) {
-        int kb0, nkb, total;
-        item_kb(item, kb0, nkb, total);
-        const int a = ti & 1;
-        const uint32_t ause = (uint32_t)(ti >> 1);
-        if (ti >= 2 && !wait(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
+    // The whole warp runs the loop with warp-uniform values and one elected lane issues each
+    // tcgen05 instruction.  Descriptors are built once; the start-address field (bits 0-13,
+    // address >> 4) is advanced by adding the byte offset >> 4 (shared addresses stay below
+    // 2^18, so the field never carries into the next one).
+    const WaiterW<> wt{abort_flag, args.err};
+    const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
+    const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
+    const uint64_t adesc0 = A_MN ? make_sdesc(smem_u32(smem + L::OFF_A), 8192, 1024)
+                                 : make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
+    const uint64_t bdesc0 = T::mn ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
+                                  : make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
+    const uint64_t bdesc0_k = make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
+    const uint64_t adesc0_k = make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
+    constexpr uint32_t A_KSTEP = A_MN ? 2048 >> 4 : 32 >> 4;
+    constexpr uint32_t B_KSTEP = T::mn ? 2048 >> 4 : 32 >> 4;
+    int it = 0, ti = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++ti) {
+      int kb0, nkb, total;
+      item_kb(item, kb0, nkb, total);
+      const int a = ti & 1;
+      const uint32_t ause = (uint32_t)(ti >> 1);
+      if (ti >= 2 && !wt(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t d_tmem = tbase + (uint32_t)(a * L::ACC_COLS);
+      for (int kb = 0; kb < total; ++kb, ++it) {
+        const int s = it % STAGES;
+        const uint32_t use = (uint32_t)(it / STAGES);
+        if (!wt(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
+        if (T::quant && !wt(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tbase + (uint32_t)(a * L::ACC_COLS);
-        for (int kb = 0; kb < total; ++kb, ++it) {
-          const int s = it % STAGES;
-          const uint32_t use = (uint32_t)(it / STAGES);
-          if (!wait(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
-          if (T::quant && !wait(&bready[s], use & 1u, kErrTimeoutReady)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
-          if (kb < nkb) {
+        const uint32_t aoff = (uint32_t)(s * L::A_BYTES) >> 4, boff = (uint32_t)(s * L::B_BYTES) >> 4;
+        if (kb < nkb) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t ad = A_MN ? make_sdesc(a_addr + kk * 2048, 8192, 1024)
-                                       : make_sdesc(a_addr + kk * 32, 16, 1024);
-              const uint64_t bd = T::mn ? make_sdesc(b_addr + kk * 2048, 8192, 1024)
-                                        : make_sdesc(b_addr + kk * 32, 16, 1024);
-              umma_bf16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-            }
-          } else {
-            umma_bf16(d_tmem, make_sdesc(a_addr, 16, 1024), make_sdesc(b_addr, 16, 1024), idesc_ext,
-                      total > 1 ? 1u : 0u);
-          }
-          umma_commit(&empty[s]);
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_bf16_w(d_tmem, adesc0 + aoff + kk * A_KSTEP, bdesc0 + boff + kk * B_KSTEP, idesc,
+                        (kb > 0 || kk > 0) ? 1u : 0u);
+        } else {
+          umma_bf16_w(d_tmem, adesc0_k + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
         }
-        if (ok) umma_commit(&tfull[a]);
+        umma_commit_w(&empty[s]);
       }
+      if (ok) umma_commit_w(&tfull[a]);
     }
   } else if (warp < 2 + R::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
-    // Each warp drains its 32 TMEM lanes (32 output rows).  TMA path (args.tma_out): 32 f32 (or
-    // 64 bf16) columns per step are written into a 128B-swizzled 32-row staging buffer and sent
-    // with one asynchronous TMA store (reduce-add when accumulating); two buffers alternate.
+    // Each warp drains 32 TMEM lanes (32 output rows); with 8 epilogue warps the two warps of a
+    // lane quarter take alternate column chunks.  TMA path (args.tma_out): 32 f32 (or 64 bf16)
+    // columns per step are written into a 128B-swizzled 32-row staging buffer and sent with one
+    // asynchronous TMA store (reduce-add when accumulating); two buffers alternate when they fit.
     // Direct path: the same staging buffer transposes each 32 x 32 block so every global store
     // is one coalesced row segment; transposed outputs are already coalesced across lanes.
     const int q = warp & 3;   // TMEM lane quarter this warp may access
+    constexpr int NH = R::EPI_WARPS / 4;   // warps per lane quarter
+    const int half = (warp - 2) / 4;       // this warp's chunks: chunk % NH == half
     uint8_t* stg = smem + L::OFF_STAGE + (warp - 2) * L::STAGE_BUFS * L::STAGE_BYTES;
-    const bool split_out = args.partial != nullptr;   // raw partial sums (reduced by a second pass)
+    const bool split_out = args.partial != nullptr;   // raw partial sums, reduced by the last split
     const int cstep = args.tma_out == 2 ? 64 : 32;
+    volatile int* last_split = reinterpret_cast<volatile int*>(tmem_slot + 2);
     int nstore = 0;
     int ti = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++ti) {
@@ -439,7 +482,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       const int rbase = m0 + 32 * q;               // first row of this warp
       const uint32_t tacc = tbase + (uint32_t)(a * L::ACC_COLS) + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += cstep) {
+      for (int c0 = half * cstep; c0 < BN; c0 += NH * cstep) {
         float f[64];
         const int nb = n0 + c0;
 #pragma unroll
@@ -498,24 +541,18 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         // ---- direct path
         const int ncols = min(min(32, BN - c0), args.N - nb);
         const int myrow = rbase + lane;
-        if (args.out && args.out_trans) {          // lanes are consecutive rows: coalesced
-          if (myrow < args.M) {
+        if (!split_out && myrow < args.M) {        // transposed outputs: lanes are consecutive rows
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {   // static indices keep f[] in registers
-              if (j >= ncols) break;
+          for (int j = 0; j < 32; ++j) {           // static indices keep f[] in registers
+            if (j >= ncols) break;
+            if (args.out && args.out_trans) {
               float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
               if (args.atomic) atomicAdd(dst, f[j]);
               else *dst = args.accumulate ? *dst + f[j] : f[j];
             }
-          }
-        }
-        if (args.out_bf && args.out_bf_trans) {
-          if (myrow < args.M) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j >= ncols) break;
-              args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j]);
-            }
+            if (args.out_bf && args.out_bf_trans)
+              args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j] * args.bf_scale);
+            if (args.out_bf_t) args.out_bf_t[(long)(nb + j) * args.ldo_bf_t + myrow] = __float2bfloat16_rn(f[j]);
           }
         }
         if (split_out || (args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
@@ -537,9 +574,29 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
               if (args.atomic) atomicAdd(dst, x);
               else *dst = args.accumulate ? *dst + x : x;
             }
-            if (args.out_bf && !args.out_bf_trans) args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x);
+            if (args.out_bf && !args.out_bf_trans)
+              args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x * args.bf_scale);
           }
           __syncwarp();
+        }
+      }
+      if (split_out) {
+        // ---- split-K: the CTA that completes the tile's last split reduces it.  Every thread
+        // makes its partial stores visible, one thread counts the split in, and the last one
+        // sums the splits in order 0, 1, ... (deterministic) from L2 and runs the epilogue.
+        __threadfence();
+        named_bar(1, 32 * R::EPI_WARPS);
+        if (warp == 2 && lane == 0) {
+          const int prev = atomicAdd(args.tile_cnt + t, 1);
+          const int last = prev == args.splits - 1;
+          if (last) args.tile_cnt[t] = 0;        // ready for the next launch
+          *last_split = last;
+        }
+        named_bar(1, 32 * R::EPI_WARPS);
+        if (*last_split) {
+          __threadfence();
+          splitk_finish(args, m0, n0, min(kBM, args.M - m0), min(BN, args.N - n0), threadIdx.x - 64,
+                        32 * R::EPI_WARPS);
         }
       }
       tc_fence_before();

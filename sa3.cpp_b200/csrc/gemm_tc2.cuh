@@ -4,7 +4,7 @@
 //   CTA r (r = %cluster_ctarank) loads rows [128 r, 128 r + 128) of the A tile and columns
 //   [r BN/2, (r+1) BN/2) of the B tile into its own shared memory (plain TMA loads: each CTA
 //   fetches only its own half, nothing is multicast), and holds rows 128 r .. of the f32
-//   accumulator in its own TMEM.  The even CTA's single MMA thread issues every
+//   accumulator in its own TMEM.  The even CTA's MMA warp (one elected lane) issues every
 //   tcgen05.mma.cta_group::2, which reads both CTAs' operand halves.
 // Each SM therefore streams 128 x 64 of A and BN/2 x 64 of B per k-block instead of 128 x 64 and
 // BN x 64: the shared-memory traffic per tensor-core cycle falls by a quarter at BN = 256, which
@@ -45,18 +45,6 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
 // TMA tile load into this CTA's shared memory whose completion is signalled on an mbarrier that
 // may live in the peer CTA of the pair (cluster address).  Not a multicast load.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* m, uint32_t bar_cluster,
@@ -82,25 +70,32 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                               uint32_t accumulate) {
+// tcgen05.mma.cta_group::2, issued warp-wide: warp-uniform operands, one elected lane issues.
+__device__ __forceinline__ void umma_bf16_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t"
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
 // Arrive once on the mbarrier at this offset in both CTAs of the pair when every MMA issued so
-// far by this thread has completed.
-__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+// far has completed (warp-wide, one elected lane).
+__device__ __forceinline__ void umma_commit_pair_w(uint64_t* bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}" ::"r"(
           smem_u32(bar)),
       "h"((uint16_t)0x3)
       : "memory");
 }
+
+constexpr int kPairEpiWarps = 8;        // two per TMEM lane quarter, alternate column chunks
+constexpr int kPairThreads = 32 * (2 + kPairEpiWarps);
 
 template <int BN, int STAGES>
 struct Gemm2Smem {
@@ -111,26 +106,27 @@ struct Gemm2Smem {
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_STAGE = align_up(OFF_B + STAGES * B_BYTES, 1024);
   static constexpr int STAGE_BYTES = 4096;
-  static constexpr int STAGE_BUFS = (OFF_STAGE + 4 * 2 * STAGE_BYTES + 1024 + 256 <= 232448) ? 2 : 1;
-  static constexpr int OFF_BAR = OFF_STAGE + 4 * STAGE_BUFS * STAGE_BYTES;
+  static constexpr int STAGE_BUFS =
+      (OFF_STAGE + kPairEpiWarps * 2 * STAGE_BYTES + (2 * STAGES + 4) * 8 + 16 + 1024 <= 232448) ? 2 : 1;
+  static constexpr int OFF_BAR = OFF_STAGE + kPairEpiWarps * STAGE_BUFS * STAGE_BYTES;
   static constexpr int BAR_BYTES = (2 * STAGES + 4) * 8 + 16;
   static constexpr int TOTAL = OFF_BAR + BAR_BYTES;
   static constexpr int DYN = TOTAL + 1024;
   static constexpr int ACC_COLS = BN;
-  static constexpr int TMEM_COLS = 2 * BN;
-  static_assert(BN == 128 || BN == 256, "pair tiles are 256 x 128 or 256 x 256");
+  static constexpr int TMEM_COLS = 2 * BN <= 256 ? 256 : 512;   // a power of two
+  static_assert(BN == 128 || BN == 192 || BN == 256, "pair tiles are 256 x 128, 192 or 256");
   static_assert(DYN <= 232448, "shared memory budget (227 KB)");
 };
 
 // BMODE 0: B is [N][K] row-major (K-major); 1: B is [K][N] row-major (MN-major).  A is [M][K].
 template <int BN, int STAGES, int BMODE>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kPairThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_ea, const __grid_constant__ CUtensorMap tm_eb,
                     const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
   using L = Gemm2Smem<BN, STAGES>;
   constexpr bool BMN = BMODE == 1;
-  constexpr int EPI_WARPS = 4;
+  constexpr int EPI_WARPS = kPairEpiWarps;
   constexpr int PM = 2 * kBM;                        // rows of a pair tile
   static_assert(!BMN || L::BH % 64 == 0, "MN-major B halves are built from 64-wide atoms");
 
@@ -232,44 +228,48 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (even CTA)
-    if (leader && lane == 0) {
+    // Warp-wide with one elected issuing lane and descriptors built once (see gemm_tc.cuh).
+    if (leader) {
+      const WaiterW<true> wt{abort_flag, args.err};
       const uint32_t idesc = make_idesc_bf16(PM, BN, 0, BMN ? 1 : 0);
       const uint32_t idesc_ext = make_idesc_bf16(PM, BN, 0, 0);
+      const uint64_t adesc0 = make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
+      const uint64_t bdesc0 = BMN ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
+                                  : make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
+      const uint64_t bdesc0_k = make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
+      constexpr uint32_t B_KSTEP = BMN ? 2048 >> 4 : 32 >> 4;
       int it = 0, ti = 0;
       bool ok = true;
       for (int t = cluster; t < ntiles && ok; t += nclusters, ++ti) {
         const int a = ti & 1;
         const uint32_t ause = (uint32_t)(ti >> 1);
-        if (ti >= 2 && !wait(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther, true)) { ok = false; break; }
+        if (ti >= 2 && !wt(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tbase + (uint32_t)(a * L::ACC_COLS);
         for (int kb = 0; kb < total; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
-          if (!wait(&full[s], use & 1u, kErrTimeoutFull, true)) { ok = false; break; }
+          if (!wt(&full[s], use & 1u, kErrTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(smem + L::OFF_A + s * L::A_BYTES);
-          const uint32_t b_addr = smem_u32(smem + L::OFF_B + s * L::B_BYTES);
+          const uint32_t aoff = (uint32_t)(s * L::A_BYTES) >> 4, boff = (uint32_t)(s * L::B_BYTES) >> 4;
           if (kb < nkb) {
 #pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk) {
-              const uint64_t ad = make_sdesc(a_addr + kk * 32, 16, 1024);
-              const uint64_t bd = BMN ? make_sdesc(b_addr + kk * 2048, 8192, 1024)
-                                      : make_sdesc(b_addr + kk * 32, 16, 1024);
-              umma_bf16_pair(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-            }
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              umma_bf16_pair_w(d_tmem, adesc0 + aoff + kk * 2u, bdesc0 + boff + kk * B_KSTEP, idesc,
+                               (kb > 0 || kk > 0) ? 1u : 0u);
           } else {
-            umma_bf16_pair(d_tmem, make_sdesc(a_addr, 16, 1024), make_sdesc(b_addr, 16, 1024), idesc_ext,
-                           total > 1 ? 1u : 0u);
+            umma_bf16_pair_w(d_tmem, adesc0 + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
           }
-          umma_commit_pair(&empty[s]);
+          umma_commit_pair_w(&empty[s]);
         }
-        if (ok) umma_commit_pair(&tfull[a]);
+        if (ok) umma_commit_pair_w(&tfull[a]);
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;
+    constexpr int NH = EPI_WARPS / 4;      // warps per TMEM lane quarter
+    const int half = (warp - 2) / 4;       // this warp's chunks: chunk % NH == half
     uint8_t* stg = smem + L::OFF_STAGE + (warp - 2) * L::STAGE_BUFS * L::STAGE_BYTES;
     const int cstep = args.tma_out == 2 ? 64 : 32;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
@@ -283,7 +283,7 @@ __global__ void __launch_bounds__(192, 1)
       const int rbase = m0 + 32 * q;
       const uint32_t tacc = tbase + (uint32_t)(a * L::ACC_COLS) + ((uint32_t)(32 * q) << 16);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += cstep) {
+      for (int c0 = half * cstep; c0 < BN; c0 += NH * cstep) {
         float f[64];
         const int nb = n0 + c0;
 #pragma unroll

@@ -1,7 +1,7 @@
 // linear.cu -- forward and backward of the adapted frozen-base linear over the tcgen05 engine.
 //
 // Forward (src/dit.h:106-147):
-//   u = x A^T                               rank-16 GEMM                      [M][16]
+//   u = x A^T                               rank-16 GEMM, written as bf16 s u [M][64] and u^T
 //   y = g * (x W^T  (+)  (s u) B^T) + bias  one GEMM: the LoRA term is a K = 16 extension of the
 //                                           base MMA chain; g (DoRA) and bias in the epilogue
 // Backward (what ggml_build_backward_expand derives for those ops, src/train_ckpt.h:400):
@@ -64,19 +64,23 @@ int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
   return k_dora_norm(c, p.pt, p.B, p.rank, p.out, p.aat, p.bns, p.m, p.s, p.nsq, p.g, err);
 }
 
+int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ext_u,
+           __nv_bfloat16* ut, int64_t ut_ld, std::string& err) {
+  GemmDesc g;   // u = x A^T  [M][16]: ext_u = bf16(s u) row-major [M][64], ut = bf16(u) as [16][ut_ld]
+  g.M = (int)M; g.N = 16; g.K = (int)in;
+  g.a = x_bf; g.lda = in;
+  g.bsrc = kB_BF16_KMAJOR; g.b = ad.a_bf; g.ldb = in;
+  g.out_bf = ext_u; g.ldo_bf = 64; g.bf_scale = ad.s;
+  g.out_bf_t = ut; g.ldo_bf_t = ut_ld;
+  g.bn = 16;
+  g.name = "lora.u";
+  return gemm(c, g, err);
+}
+
 int linear_forward(Ctx* c, const LinearFwd& f, std::string& err) {
   const Weight* w = f.w;
   const AdapterPrep* ad = f.ad;
-  if (ad) {
-    GemmDesc g;   // u = x A^T  [M][16]
-    g.M = (int)f.M; g.N = 16; g.K = (int)w->in;
-    g.a = f.x_bf; g.lda = w->in;
-    g.bsrc = kB_BF16_KMAJOR; g.b = ad->a_bf; g.ldb = w->in;
-    g.out = f.u; g.ldo = 16; g.bn = 16;
-    g.name = "lora.u";
-    if (gemm(c, g, err)) return 1;
-    if (k_pack_rank(c, f.u, (int)f.M, ad->s, f.ext_u, 1.0f, f.ut, (int)f.ut_ld, err)) return 1;
-  }
+  if (ad && lora_u(c, f.x_bf, f.M, w->in, *ad, f.ext_u, f.ut, f.ut_ld, err)) return 1;
   GemmDesc g;   // y = g * (x W^T + s u B^T) + bias
   g.M = (int)f.M; g.N = (int)w->out; g.K = (int)w->in;
   g.a = f.x_bf; g.lda = w->in;
@@ -104,15 +108,16 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
       return 1;
   }
   if (ad) {
-    GemmDesc g;   // du = s dz B  [M][16]
+    GemmDesc g;   // du = s dz B  [M][16]: ext_du row-major [M][64] and dut [16][ut_ld], both bf16
     g.M = (int)b.M; g.N = 16; g.K = (int)out;
     g.a = b.dz; g.lda = out;
     g.bsrc = kB_BF16_KMAJOR; g.b = ad->bt_bf; g.ldb = out;
     g.alpha = ad->s;
-    g.out = b.du; g.ldo = 16; g.bn = 16;
+    g.out_bf = b.ext_du; g.ldo_bf = 64;
+    g.out_bf_t = b.dut; g.ldo_bf_t = b.ut_ld;
+    g.bn = 16;
     g.name = "lora.du";
     if (gemm(c, g, err)) return 1;
-    if (k_pack_rank(c, b.du, (int)b.M, 1.0f, b.ext_du, 1.0f, b.dut, (int)b.ut_ld, err)) return 1;
   }
   if (b.dx || b.dx_bf) {
     GemmDesc g;   // dx = dz W + du A

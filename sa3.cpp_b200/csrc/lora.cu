@@ -29,25 +29,6 @@ __global__ void cvt_bf16_kernel(const float* __restrict__ src, int64_t n, __nv_b
     dst[i] = __float2bfloat16_rn(src[i]);
 }
 
-// in f32 [rows][16] -> ext bf16 [rows][64] (mul * in in columns 0..15, zeros after) and, if
-// trans is non-null, bf16 [16][ld_trans] with trans[r][row] = mul_t * in[row][r].
-__global__ void pack_rank_kernel(const float* __restrict__ in, int rows, float mul,
-                                 __nv_bfloat16* __restrict__ ext, float mul_t,
-                                 __nv_bfloat16* __restrict__ trans, int ld_trans) {
-  const int row = blockIdx.x * blockDim.y + threadIdx.y;
-  if (row >= rows) return;
-  const int l = threadIdx.x;   // 0..31: two output columns each
-  if (ext) {
-    float a = 0.f, b = 0.f;
-    if (l < 8) {
-      a = mul * in[row * R + 2 * l];
-      b = mul * in[row * R + 2 * l + 1];
-    }
-    reinterpret_cast<uint32_t*>(ext + (int64_t)row * 64)[l] = pack_bf16x2(a, b);
-  }
-  if (trans && l < R) trans[(int64_t)l * ld_trans + row] = __float2bfloat16_rn(mul_t * in[row * R + l]);
-}
-
 // Adapter operand forms.  A f32 [rank][in], B f32 [out][rank].
 //   a_bf  bf16 [16][in]    (rows >= rank zero)      B operand of u = x A^T, A operand of W A^T
 //   at_x  bf16 [in][64]    A^T in columns 0..15     K-extension B operand of dx
@@ -436,14 +417,6 @@ int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::str
   ProfScope prof_(c, "cvt_bf16");
   cvt_bf16_kernel<<<grid1d(n / 4 + 1, 256), 256, 0, c->stream>>>(src, n, dst);
   return check_launch("cvt_bf16", err);
-}
-
-int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
-                __nv_bfloat16* trans, int ld_trans, std::string& err) {
-  ProfScope prof_(c, "pack_rank");
-  dim3 blk(32, 8);
-  pack_rank_kernel<<<(unsigned)((rows + 7) / 8), blk, 0, c->stream>>>(in, rows, mul, ext, mul_t, trans, ld_trans);
-  return check_launch("pack_rank", err);
 }
 
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,

@@ -23,8 +23,6 @@ int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::str
 int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
-int k_pack_rank(Ctx* c, const float* in, int rows, float mul, __nv_bfloat16* ext, float mul_t,
-                __nv_bfloat16* trans, int ld_trans, std::string& err);
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err);

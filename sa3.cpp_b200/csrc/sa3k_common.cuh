@@ -155,6 +155,52 @@ __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
+// Cluster-scope (acquire.cluster) form of mbar_try_wait, for barriers that a peer CTA's
+// operations complete.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Warp-wide bounded wait: every lane of the warp calls it and all get the same answer (the
+// warp stays converged for the .aligned tcgen05 instructions and elect.sync issues that
+// follow).  CLUSTER selects the cluster-scope acquire.
+template <bool CLUSTER = false>
+struct WaiterW {
+  volatile int* abort_flag;
+  int* err;
+  __device__ __forceinline__ bool probe(uint32_t a, uint32_t parity) const {
+    return CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity);
+  }
+  __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity, int code) const {
+    const uint32_t a = smem_u32(bar);
+    if (__all_sync(0xffffffffu, probe(a, parity))) return true;   // fast path: already complete
+    if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t i = 0;; ++i) {
+      if (__all_sync(0xffffffffu, probe(a, parity))) return true;
+      if ((i & 63u) == 63u) {
+        if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
+        if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitLimitNs)) {
+          if ((threadIdx.x & 31) == 0) {
+            record_error(err, code);
+            *abort_flag = 1;
+          }
+          __syncwarp();
+          return false;
+        }
+      }
+    }
+  }
+};
+
 // D(tmem) (+)= A(smem desc) * B(smem desc), bf16 in, f32 accumulate.
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                           uint32_t idesc, uint32_t accumulate) {

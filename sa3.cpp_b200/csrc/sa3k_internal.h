@@ -57,7 +57,7 @@ struct Ctx {
   bool weight_cache = true;          // quantized weights keep a dequantized bf16 operand copy
   bool smem_dequant = false;         // force the in-smem dequant GEMM path for quantized weights
   int tile_n = 0;                    // main-GEMM N tile: 0 = cost model, 128 or 256 = fixed
-  bool gemm_pair = true;             // CTA-pair (cta_group::2) GEMMs where they fit
+  int gemm_pair = 1;                 // CTA-pair (cta_group::2) GEMMs: 0 never, 1 where they pay, 2 always
   bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
   // NeoX RoPE (cos, sin) table for (positions, rot, base), kept in scratch slot kSlotRope
   const void* rope_tab = nullptr;
@@ -94,7 +94,7 @@ inline int check_launch(const char* what, std::string& err) {
 }
 
 // Scratch slots owned by a context (see api.cu for the linear path's slots).
-enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61 };
+enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61, kSlotSplitCnt = 60 };
 
 // Scratch slot `slot` of at least `bytes` (grows; contents are not preserved on growth).
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
@@ -135,9 +135,12 @@ struct GemmDesc {
   long ldo = 0;
   int out_trans = 0;
   int accumulate = 0;
-  __nv_bfloat16* out_bf = nullptr;
+  __nv_bfloat16* out_bf = nullptr;    // bf_scale * the f32 value, row-major or (out_bf_trans) transposed
   long ldo_bf = 0;
   int out_bf_trans = 0;
+  float bf_scale = 1.0f;
+  __nv_bfloat16* out_bf_t = nullptr;  // the unscaled value again as bf16, transposed [N][ldo_bf_t]
+  long ldo_bf_t = 0;
   int bn = 128;         // N tile (16, 128)
   // split-K partial sums may be added into `out` with f32 atomics (no reduction pass; the
   // summation order, and so the last bits, vary from run to run).  f32 `out` only.

@@ -1,0 +1,82 @@
+"""Single-kernel cases for profiling and tuning: one frozen-base linear of a chosen shape, run a
+few times through the C ABI, so that a profiler (ncu -k regex:gemm_tc -c 1) sees a handful of
+launches of one GEMM on inputs larger than L2 and a few hundred MB on the device.
+
+    python sa3.cpp_b200/kernel_cases.py gemm --m 4352 --n 1536 --k 1536 [--dx] [--qtype q8_0]
+        [--pair 0|1] [--tile-n 0|128|192|256] [--reps 3] [--time]
+
+--dx runs the input-gradient GEMM dx[m][k] = dy[m][n] . W[n][k] of a linear with in = k,
+out = n (the weight is used transposed); the default is the forward y = x W^T + 0.
+--time prints the CUDA-event time per launch (not to be used under a profiler)."""
+import argparse
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def gemm_case(a):
+    import numpy as np
+    import torch
+    import sa3k
+    import gguf_blocks
+    torch.cuda.set_device(0)
+    ctx = sa3k.Context(0)
+    ctx.set_option(sa3k.OPT_GEMM_PAIR, a.pair)
+    ctx.set_option(sa3k.OPT_GEMM_TILE_N, a.tile_n)
+    g = torch.Generator().manual_seed(0)
+    W = torch.randn(a.n, a.k, generator=g) * 0.02                 # [out = n][in = k]
+    if a.qtype == "f32":
+        w = ctx.upload(W.numpy().view(np.uint8).reshape(a.n, -1), "f32", a.k, a.n)
+    else:
+        w = ctx.upload(gguf_blocks.encode(W.numpy(), a.qtype), a.qtype, a.k, a.n)
+    dev = torch.device("cuda", 0)
+    x = torch.randn(a.m, a.k, device=dev)
+    y = torch.empty(a.m, a.n, device=dev)
+    if a.dx:
+        dy = torch.randn(a.m, a.n, device=dev)
+        dx = torch.empty(a.m, a.k, device=dev)
+        run = lambda: ctx.linear_bwd(w, x, y, dy, dx)
+        flops = 2.0 * a.m * a.n * a.k
+    else:
+        run = lambda: ctx.linear_fwd(w, x, y)
+        flops = 2.0 * a.m * a.n * a.k
+    for _ in range(a.warmup):
+        run()
+    ctx.sync()
+    if a.time:
+        ctx.profile_enable(timing=1)
+    for _ in range(a.reps):
+        run()
+    ctx.sync()
+    if a.time:
+        pr = ctx.profile_read()
+        name = "linear.dx" if a.dx else "linear.fwd"
+        n, ms = pr[name]
+        print(f"{'dx' if a.dx else 'fwd'} {a.m}x{a.n}x{a.k} {a.qtype} pair{a.pair} bn{a.tile_n}: "
+              f"{ms / n * 1e3:.1f} us/launch, {flops * n / (ms / 1e3) / 1e12:.1f} TFLOP/s")
+    w.free()
+    ctx.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="case", required=True)
+    gp = sub.add_parser("gemm")
+    gp.add_argument("--m", type=int, default=4352)
+    gp.add_argument("--n", type=int, default=1536)
+    gp.add_argument("--k", type=int, default=1536)
+    gp.add_argument("--dx", action="store_true")
+    gp.add_argument("--qtype", default="f32", choices=["f32", "q8_0", "q4_k"])
+    gp.add_argument("--pair", type=int, default=1)
+    gp.add_argument("--tile-n", type=int, default=0)
+    gp.add_argument("--warmup", type=int, default=2)
+    gp.add_argument("--reps", type=int, default=3)
+    gp.add_argument("--time", action="store_true")
+    a = ap.parse_args()
+    if a.case == "gemm":
+        gemm_case(a)
+
+
+if __name__ == "__main__":
+    main()
