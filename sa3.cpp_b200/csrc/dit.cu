@@ -20,6 +20,7 @@
 //    src/train_ckpt.h:292-317); targets must be per-block projections.
 #include "../../include/sa3k.h"
 #include "attention.h"
+#include "gemm_r16.h"
 #include "linear.h"
 #include "lora_kernels.h"
 
@@ -39,6 +40,12 @@ struct DitTarget {
   int64_t offA = 0, offB = 0, offM = -1;   // into the flat adapter state
   float* bns = nullptr;                    // [out]
   AdapterPrep prep;
+  // the step's inputs of the grouped adapter-gradient pass (activation arena): dz [M][out] bf16,
+  // dg [out], du^T [16][ut_ld] bf16, cb [16][out] bf16 (dora), c3 [16][16]; and the forward's
+  // input rows x_bf [M][in] and u^T of this linear
+  __nv_bfloat16 *dz = nullptr, *dut = nullptr, *cb = nullptr;
+  float *dg = nullptr, *c3 = nullptr;
+  const __nv_bfloat16 *x_bf = nullptr, *ut = nullptr;
 };
 
 struct DitBlockAct {
@@ -71,6 +78,10 @@ struct DitModel {
   void* prep_mem = nullptr;
   PrepDesc* prep_desc = nullptr;       // device descriptors of the adapters (grouped preparation)
   int64_t max_out = 0;
+  // grouped rank-16 GEMMs: DoRA P = W A^T of every adapter (forward preparation) and every
+  // adapter's dB / dA contractions (end of the backward); bound to the activation arena
+  R16Group r16_prep, r16_grads;
+  float* c3_all = nullptr;
   // activations for shape (B, T, C)
   int B = 0, T = 0, C = 0;
   void* arena = nullptr;
@@ -97,6 +108,8 @@ struct DitModel {
   int64_t ut_ld = 0;
 
   ~DitModel() {
+    r16_group_free(r16_prep);
+    r16_group_free(r16_grads);
     for (void* q : owned) cudaFree(q);
     if (arena) cudaFree(arena);
     for (sa3k_weight* h : weights) sa3k_weight_free(h);
@@ -126,6 +139,85 @@ static void* dmalloc(DitModel& m, size_t bytes, std::string& err) {
   }
   m.owned.push_back(q);
   return q;
+}
+
+// ------------------------------------------------------------------ grouped adapter passes
+// After the activation arena moved: bind every adapter to its block's input rows and u^T, refresh
+// the device descriptors (now with the gradient pointers), and build the grouped rank-16 GEMMs
+// of the DoRA preparation and of the adapter gradients.
+static const char* const kTargetKinds[4] = {"self.qkv.weight", "self.out.weight", "ff.proj.weight", "ff.out.weight"};
+
+static int bind_adapter_grads(DitModel& m, std::string& err) {
+  for (DitTarget& t : m.tg) { t.x_bf = nullptr; t.ut = nullptr; }
+  for (int l = 0; l < m.cfg.depth; ++l) {
+    DitBlockAct& a = m.blk[(size_t)l];
+    const __nv_bfloat16* xs[4] = {a.h_a, a.oa, a.hf, a.act};
+    for (int j = 0; j < 4; ++j) {
+      auto it = m.tix.find("dit." + std::to_string(l) + "." + kTargetKinds[j]);
+      if (it == m.tix.end()) continue;
+      DitTarget& t = m.tg[(size_t)it->second];
+      t.x_bf = xs[j];
+      t.ut = a.ut[j];
+    }
+  }
+  std::vector<PrepDesc> descs;
+  std::vector<R16Job> prep, grads;
+  for (DitTarget& t : m.tg) {
+    if (!t.x_bf) {
+      err = "adapter target " + t.name + " is not a per-block self-attention or feed-forward projection";
+      return 1;
+    }
+    const AdapterPrep& p = t.prep;
+    PrepDesc pd{};
+    pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
+    pd.rank = p.rank; pd.dora = p.dora() ? 1 : 0; pd.s = p.s; pd.in = p.in; pd.out = p.out;
+    pd.a_bf = p.a_bf; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_bf = p.bt_bf;
+    pd.pt = p.pt; pd.aat = p.aat; pd.nsq = p.nsq; pd.g = p.g;
+    pd.dg = t.dg; pd.dB = m.g + t.offB; pd.dA = m.g + t.offA; pd.dm = t.offM >= 0 ? m.g + t.offM : nullptr;
+    pd.cb = t.cb; pd.c3 = t.c3;
+    descs.push_back(pd);
+    const int64_t M = (int64_t)m.B * m.Sfull();
+    R16Job j;
+    // dB [out][rank] += s dz^T u     (A = dz read MN-major, K = the M token rows)
+    j = R16Job();
+    j.a = t.dz; j.lda = t.out; j.a_mn = 1; j.M = (int)t.out; j.N = p.rank; j.K = (int)M;
+    j.b = t.ut; j.ldb = m.ut_ld; j.alpha = p.s;
+    j.out = m.g + t.offB; j.ldo = p.rank; j.atomic = 1;
+    grads.push_back(j);
+    // dA [rank][in] += du^T x        (A = x read MN-major, stored transposed)
+    j = R16Job();
+    j.a = t.x_bf; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)M;
+    j.b = t.dut; j.ldb = m.ut_ld;
+    j.out = m.g + t.offA; j.ldo = t.in; j.out_trans = 1; j.atomic = 1;
+    grads.push_back(j);
+    if (p.dora() && t.w->bf16) {
+      // dA += (dt2 B)^T W             (A = the bf16 base copy read MN-major, K = out)
+      j = R16Job();
+      j.a = t.w->bf16; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)t.out;
+      j.b = t.cb; j.ldb = t.out;
+      j.out = m.g + t.offA; j.ldo = t.in; j.out_trans = 1; j.atomic = 1;
+      grads.push_back(j);
+      // P^T [16][out] = (W A^T)^T
+      j = R16Job();
+      j.a = t.w->bf16; j.lda = t.in; j.a_mn = 0; j.M = (int)t.out; j.N = 16; j.K = (int)t.in;
+      j.b = p.a_bf; j.ldb = t.in;
+      j.out = p.pt; j.ldo = t.out; j.out_trans = 1; j.atomic = 0;
+      prep.push_back(j);
+    }
+  }
+  if (cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+    err = "adapter descriptor upload failed";
+    return 1;
+  }
+  // every DoRA base needs its bf16 copy for the grouped P and dA terms (else the per-adapter
+  // GEMMs over the quantized codes run instead)
+  bool all_bf16 = true;
+  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (!t.prep.dora() || t.w->bf16);
+  r16_group_free(m.r16_prep);
+  r16_group_free(m.r16_grads);
+  if (!all_bf16) return 0;
+  if (r16_group_build(m.c, prep, 24, m.r16_prep, err)) return 1;
+  return r16_group_build(m.c, grads, 24, m.r16_grads, err);
 }
 
 // ------------------------------------------------------------------ activation arena
@@ -175,6 +267,13 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     const int64_t maxout = std::max<int64_t>(wide, 6 * D);
     m.dg = f(maxout); m.c3 = f(256);
     m.ext_u = h(M * 64); m.ext_du = h(M * 64); m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
+    m.c3_all = f(256 * (int64_t)m.tg.size());
+    for (size_t i = 0; i < m.tg.size(); ++i) {
+      DitTarget& t = m.tg[i];
+      t.dz = h(M * t.out); t.dg = f(t.out); t.dut = h(16 * m.ut_ld);
+      t.cb = m.dora ? h(16 * t.out) : nullptr;
+      t.c3 = m.c3_all ? m.c3_all + 256 * (int64_t)i : nullptr;
+    }
     if (pass == 0) {
       m.arena_bytes = off;
       if (cudaMalloc(&m.arena, off) != cudaSuccess) {
@@ -185,7 +284,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       }
     }
   }
-  return 0;
+  return bind_adapter_grads(m, err);
 }
 
 // ------------------------------------------------------------------ linear helpers
@@ -197,7 +296,7 @@ static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float
   return linear_forward(m.c, f, err);
 }
 
-// dy == nullptr: m.dz (and m.dg for dora) were written by a fused producer of the gradient
+// dy == nullptr: dz_of(t) (and dg_of(t) for dora) were written by a fused producer of the gradient
 static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
                    const float* y, const float* dy, int64_t M, const __nv_bfloat16* ut, float* dx, int dx_acc,
                    __nv_bfloat16* dx_bf, std::string& err) {
@@ -210,6 +309,11 @@ static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias
     b.grad_accumulate = 1;
   }
   b.dz = m.dz; b.dg = m.dg; b.ext_du = m.ext_du; b.dut = m.dut; b.cb = m.cb; b.c3 = m.c3;
+  if (t && m.r16_grads.table) {
+    // keep this adapter's dz / dg / du^T for the grouped gradient pass at the end of the backward
+    b.dz = t->dz; b.dg = t->dg; b.dut = t->dut;
+    b.defer_grads = true;
+  }
   return linear_backward(m.c, b, err);
 }
 
@@ -226,6 +330,10 @@ static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_b
   if (k_silu_bf16(m.c, h, M * w0->out, hb, err)) return 1;
   return lin_fwd(m, w2, nullptr, b2, hb, M, y, y_bf, nullptr, err);
 }
+
+// where the backward of linear `t` (null: a linear without adapter) expects its dz / dg
+static __nv_bfloat16* dz_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dz : m.dz; }
+static float* dg_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dg : m.dg; }
 
 static DitTarget* target(DitModel& m, const std::string& name) {
   auto it = m.tix.find(name);
@@ -248,8 +356,12 @@ static int dit_step(DitModel& m, std::string& err) {
   if (k_prep_all(c, m.prep_desc, nt, err)) return 1;
   if (m.dora) {
     if (k_aat_all(c, m.prep_desc, nt, err)) return 1;
-    for (DitTarget& t : m.tg)
-      if (adapter_dora_p(c, t.w, t.prep, err)) return 1;
+    if (m.r16_prep.table) {
+      if (r16_group_run(c, m.r16_prep, "dora.P", err)) return 1;
+    } else {
+      for (DitTarget& t : m.tg)
+        if (adapter_dora_p(c, t.w, t.prep, err)) return 1;
+    }
     if (k_dora_norm_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
   }
 
@@ -390,11 +502,11 @@ static int dit_step(DitModel& m, std::string& err) {
     // feed-forward branch
     // (the gate and SwiGLU backward write the adapted linears' dz / dg directly)
     if (k_gate_bwd_dz(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, a.yf, b_fo, tf && tf->prep.dora() ? tf->prep.g : nullptr,
-                      m.dz, m.dg, err))
+                      dz_of(m, tf), dg_of(m, tf), err))
       return 1;
     if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, a.ut[3], m.dact, 0, nullptr, err)) return 1;
-    if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, m.dz, m.dg,
-                        err))
+    if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, dz_of(m, tp),
+                        dg_of(m, tp), err))
       return 1;
     if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, err)) return 1;
@@ -420,7 +532,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, err)) return 1;
     // self-attention branch
     if (k_gate_bwd_dz(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, a.yo, nullptr,
-                      to && to->prep.dora() ? to->prep.g : nullptr, m.dz, m.dg, err))
+                      to && to->prep.dora() ? to->prep.g : nullptr, dz_of(m, to), dg_of(m, to), err))
       return 1;
     if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, nullptr, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
     {
@@ -445,6 +557,18 @@ static int dit_step(DitModel& m, std::string& err) {
     }
     if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, m.dq3, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, err)) return 1;
+  }
+  // ---------------- adapter gradients, grouped over every adapter of the step: the DoRA row terms
+  // (dm, dB, and the cb / c3 factors of dA), then one launch for all dB += s dz^T u,
+  // dA += du^T x and dA += cb W contractions, then dA += 2 c3 A
+  if (m.r16_grads.table) {
+    if (m.dora) {
+      if (cudaMemsetAsync(m.c3_all, 0, sizeof(float) * 256 * m.tg.size(), c->stream) != cudaSuccess)
+        return check_launch("memset", err);
+      if (k_dora_bwd_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
+    }
+    if (r16_group_run(c, m.r16_grads, "lora.grads", err)) return 1;
+    if (m.dora && k_dora_da_c3_all(c, m.prep_desc, nt, err)) return 1;
   }
   return 0;
 }

@@ -130,7 +130,7 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
     g.name = "linear.dx";
     if (gemm(c, g, err)) return 1;
   }
-  if (!ad) return 0;
+  if (!ad || b.defer_grads) return 0;
   // The rank-16 gradient GEMMs run with the long dimension as M (full 128-row MMA tiles) and
   // add their split-K parts into the gradient with atomics.
   {

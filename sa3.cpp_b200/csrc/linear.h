@@ -61,6 +61,8 @@ struct LinearBwd {
   const float* y = nullptr;            // forward output [M][out] (needed by dora-rows)
   const float* dy = nullptr;           // upstream gradient [M][out] f32
   bool dz_ready = false;               // dz (and dg for dora) already written by a fused producer
+  bool defer_grads = false;            // stop after dx: the caller computes dA / dB / dm later
+                                       // (grouped over many adapters) from dz, dg, dut and u^T
   int64_t M = 0;
   const __nv_bfloat16* ut = nullptr;   // u^T from the forward [16][ut_ld] (adapter)
   int64_t ut_ld = 0;

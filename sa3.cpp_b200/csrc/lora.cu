@@ -337,18 +337,19 @@ __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* _
 // go to shared memory).  Phase 2: thread (r, k), r <= k < R, sums dt3 B[o][r] B[o][k] over the
 // block's rows and adds it to c3 (one atomic per entry and block).
 constexpr int kDoraRows = 128;
-__global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
-    const float* __restrict__ pt, const float* __restrict__ B, int rank, int64_t out, const float* __restrict__ aat,
-    const float* __restrict__ nsq, const float* __restrict__ g, const float* __restrict__ dg, float s,
-    float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __nv_bfloat16* __restrict__ cb,
-    float* __restrict__ c3) {
+__device__ __forceinline__ void dora_bwd_rows(int blk, const float* __restrict__ pt, const float* __restrict__ B,
+                                              int rank, int64_t out, const float* __restrict__ aat,
+                                              const float* __restrict__ nsq, const float* __restrict__ g,
+                                              const float* __restrict__ dg, float s, float* __restrict__ dm,
+                                              int dm_accumulate, float* __restrict__ dB,
+                                              __nv_bfloat16* __restrict__ cb, float* __restrict__ c3) {
   __shared__ float saat[R * R];
   __shared__ float sb[kDoraRows][R + 1];    // B[o][:]          (+1: no bank conflicts on columns)
   __shared__ float sbt[kDoraRows][R + 1];   // dt3[o] B[o][:]
   for (int e = threadIdx.x; e < R * R; e += blockDim.x) saat[e] = aat[e];
   __syncthreads();
   const int row = threadIdx.x;
-  const int64_t o = (int64_t)blockIdx.x * kDoraRows + row;
+  const int64_t o = (int64_t)blk * kDoraRows + row;
   float b[R];
   float dt3 = 0.f;
 #pragma unroll
@@ -378,7 +379,7 @@ __global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
   }
   __syncthreads();
   // 136 (r <= k) entries of the symmetric R x R block sum
-  const int nrows = (int)min((int64_t)kDoraRows, out - (int64_t)blockIdx.x * kDoraRows);
+  const int nrows = (int)min((int64_t)kDoraRows, out - (int64_t)blk * kDoraRows);
   for (int e = threadIdx.x; e < R * (R + 1) / 2; e += blockDim.x) {
     int r = 0, rem = e;
     while (rem >= R - r) { rem -= R - r; ++r; }
@@ -388,6 +389,40 @@ __global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
     for (int q = 0; q < nrows; ++q) acc = fmaf(sbt[q][r], sb[q][k], acc);
     atomicAdd(c3 + r * R + k, acc);
     if (k != r) atomicAdd(c3 + k * R + r, acc);
+  }
+}
+
+__global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
+    const float* __restrict__ pt, const float* __restrict__ B, int rank, int64_t out, const float* __restrict__ aat,
+    const float* __restrict__ nsq, const float* __restrict__ g, const float* __restrict__ dg, float s,
+    float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __nv_bfloat16* __restrict__ cb,
+    float* __restrict__ c3) {
+  dora_bwd_rows(blockIdx.x, pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_accumulate, dB, cb, c3);
+}
+
+// All DoRA adapters of a group at once: blockIdx.y = adapter, blockIdx.x = 128-row block of its
+// output rows (blocks past an adapter's rows return at once).  dm, dB accumulate.
+__global__ void __launch_bounds__(kDoraRows) dora_bwd_all_kernel(const PrepDesc* __restrict__ descs) {
+  const PrepDesc& d = descs[blockIdx.y];
+  if (!d.dora || (int64_t)blockIdx.x * kDoraRows >= d.out) return;
+  dora_bwd_rows(blockIdx.x, d.pt, d.B, d.rank, d.out, d.aat, d.nsq, d.g, d.dg, d.s, d.dm, 1, d.dB, d.cb, d.c3);
+}
+
+// dA[r][i] += 2 sum_q c3[r][q] A[q][i] for all DoRA adapters: blockIdx.y = adapter, 256 (r, i)
+// entries per block.
+__global__ void dora_da_c3_all_kernel(const PrepDesc* __restrict__ descs) {
+  const PrepDesc& d = descs[blockIdx.y];
+  if (!d.dora) return;
+  __shared__ float s3[R * R];
+  if (threadIdx.x < R * R) s3[threadIdx.x] = d.c3[threadIdx.x];
+  __syncthreads();
+  const int64_t n = (int64_t)d.rank * d.in;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(k / d.in);
+    const int64_t i = k % d.in;
+    float acc = 0.f;
+    for (int q = 0; q < d.rank; ++q) acc = fmaf(s3[r * R + q], d.A[(int64_t)q * d.in + i], acc);
+    d.dA[k] += 2.f * acc;
   }
 }
 
@@ -495,6 +530,19 @@ int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::
   ProfScope prof_(c, "dora_norm");
   dora_norm_all_kernel<<<dim3((unsigned)((max_out + 255) / 256), (unsigned)n), 256, 0, c->stream>>>(descs);
   return check_launch("dora_norm_all", err);
+}
+
+int k_dora_bwd_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err) {
+  ProfScope prof_(c, "dora_bwd");
+  dora_bwd_all_kernel<<<dim3((unsigned)((max_out + kDoraRows - 1) / kDoraRows), (unsigned)n), kDoraRows, 0,
+                        c->stream>>>(descs);
+  return check_launch("dora_bwd_all", err);
+}
+
+int k_dora_da_c3_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
+  ProfScope prof_(c, "dora_da_c3");
+  dora_da_c3_all_kernel<<<dim3(64, (unsigned)n), 256, 0, c->stream>>>(descs);
+  return check_launch("dora_da_c3_all", err);
 }
 
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err) {

@@ -16,6 +16,12 @@ struct PrepDesc {
   int64_t in, out;
   __nv_bfloat16 *a_bf, *at_x, *b_x, *bt_bf;
   float *pt, *aat, *nsq, *g;
+  // gradients (grouped DoRA backward): dg [out] in, dm [out] / dB [out][rank] / dA [rank][in]
+  // accumulated, cb [16][out] bf16 and c3 [16][16] (zeroed before) out
+  const float* dg;
+  float *dm, *dB, *dA;
+  __nv_bfloat16* cb;
+  float* c3;
 };
 
 int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err);
@@ -23,6 +29,9 @@ int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::str
 int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
+// grouped DoRA backward (dm, dB, cb, c3 from dg) and the dA += 2 c3 A term, over n adapters
+int k_dora_bwd_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
+int k_dora_da_c3_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err);
