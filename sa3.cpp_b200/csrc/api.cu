@@ -45,7 +45,7 @@ void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err) {
 
 // Scratch slots of the C-ABI linear entry points.
 enum Slot : int {
-  kS_XBF = 0, kS_PREP, kS_EXTU, kS_UT, kS_DZ, kS_DG, kS_EXTDU, kS_DUT, kS_CB, kS_C3, kS_HOST_IO, kS_OPT,
+  kS_XBF = 0, kS_PREP, kS_UT, kS_DZ, kS_DG, kS_DUT, kS_CB, kS_C3, kS_HOST_IO, kS_OPT,
   kS_COUNT
 };
 
@@ -78,7 +78,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (k_cvt_bf16(c, x, S * in, x_bf, err)) return 1;
 
   AdapterPrep prep;
-  __nv_bfloat16 *ext_u = nullptr, *ut = nullptr;
+  __nv_bfloat16* ut = nullptr;
   if (adapter) {
     prep.rank = ad->rank; prep.in = in; prep.out = out; prep.s = ad->scale;
     prep.A = ad->A; prep.B = ad->B; prep.m = dora ? ad->magnitude : nullptr; prep.bns = ad->base_norm_sq;
@@ -86,17 +86,17 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
     if (!mem) return 1;
     adapter_bind(prep, mem);
     if (adapter_prepare(c, w, prep, err)) return 1;
-    if (!get(c, kS_EXTU, S * 64, ext_u, err) || !get(c, kS_UT, 16 * s_pad, ut, err))
+    if (!get(c, kS_UT, 16 * s_pad, ut, err))
       return 1;
   }
   if (fwd || (bwd && adapter)) {
     // the backward needs u^T, which the forward produces; a backward-only call recomputes it
     LinearFwd f;
     f.w = w; f.ad = adapter ? &prep : nullptr; f.bias = bias; f.x_bf = x_bf; f.M = S;
-    f.y = y_out; f.ext_u = ext_u; f.ut = ut; f.ut_ld = s_pad;
+    f.y = y_out; f.ut = ut; f.ut_ld = s_pad;
     if (!fwd) {
       // u only (the main GEMM is skipped without an output)
-      if (lora_u(c, x_bf, S, in, prep, ext_u, ut, s_pad, err)) return 1;
+      if (lora_u(c, x_bf, S, in, prep, ut, s_pad, err)) return 1;
     } else if (linear_forward(c, f, err)) {
       return 1;
     }
@@ -110,9 +110,7 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (!get(c, kS_DZ, S * out, b.dz, err)) return 1;
   if (dora && (!get(c, kS_DG, out, b.dg, err) || !get(c, kS_CB, 16 * out, b.cb, err) || !get(c, kS_C3, 256, b.c3, err)))
     return 1;
-  if (adapter && (!get(c, kS_EXTDU, S * 64, b.ext_du, err) ||
-                  !get(c, kS_DUT, 16 * s_pad, b.dut, err)))
-    return 1;
+  if (adapter && !get(c, kS_DUT, 16 * s_pad, b.dut, err)) return 1;
   return linear_backward(c, b, err);
 }
 

@@ -104,7 +104,7 @@ struct DitModel {
   __nv_bfloat16* dO_b = nullptr;
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
-  __nv_bfloat16 *ext_u = nullptr, *ext_du = nullptr, *dut = nullptr, *dz = nullptr, *cb = nullptr;
+  __nv_bfloat16 *dut = nullptr, *dz = nullptr, *cb = nullptr;
   int64_t ut_ld = 0;
 
   ~DitModel() {
@@ -266,7 +266,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
     const int64_t maxout = std::max<int64_t>(wide, 6 * D);
     m.dg = f(maxout); m.c3 = f(256);
-    m.ext_u = h(M * 64); m.ext_du = h(M * 64); m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
+    m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
     m.c3_all = f(256 * (int64_t)m.tg.size());
     for (size_t i = 0; i < m.tg.size(); ++i) {
       DitTarget& t = m.tg[i];
@@ -292,7 +292,7 @@ static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float
                    int64_t M, float* y, __nv_bfloat16* y_bf, __nv_bfloat16* ut, std::string& err) {
   LinearFwd f;
   f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_bf = x; f.M = M; f.y = y; f.y_bf = y_bf;
-  f.ext_u = m.ext_u; f.ut = ut; f.ut_ld = m.ut_ld;
+  f.ut = ut; f.ut_ld = m.ut_ld;
   return linear_forward(m.c, f, err);
 }
 
@@ -308,7 +308,7 @@ static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias
     b.dA = m.g + t->offA; b.dB = m.g + t->offB; b.dm = t->offM >= 0 ? m.g + t->offM : nullptr;
     b.grad_accumulate = 1;
   }
-  b.dz = m.dz; b.dg = m.dg; b.ext_du = m.ext_du; b.dut = m.dut; b.cb = m.cb; b.c3 = m.c3;
+  b.dz = m.dz; b.dg = m.dg; b.dut = m.dut; b.cb = m.cb; b.c3 = m.c3;
   if (t && m.r16_grads.table) {
     // keep this adapter's dz / dg / du^T for the grouped gradient pass at the end of the backward
     b.dz = t->dz; b.dg = t->dg; b.dut = t->dut;

@@ -100,20 +100,23 @@ __global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __r
   tab[e] = make_float2(cs, sn);
 }
 
-__device__ __forceinline__ void rope_cs(const float2* __restrict__ tab, int pos, int i, int rot, float& c, float& s) {
-  const float2 v = tab[pos * (rot / 2) + i];
-  c = v.x;
-  s = v.y;
-}
-
-// One warp per (token, head, slice); lane l holds head elements l and l + 32.
+// One warp per (slice, head) and kHeadRows consecutive token rows; lane l holds head elements
+// 2l and 2l + 1 (one 8-byte load and one 4-byte bf16x2 store per row).  All rows' loads are
+// issued before any row is processed.  RoPE partners: rot 32 pairs (i, i + 16), i < 16, live in
+// lanes l and l ^ 8 (lanes 0..15); rot 64 pairs (i, i + 32) in lanes l and l ^ 16.
 struct HeadSlices {
   HeadSlice s[5];
   int n;
 };
+constexpr int kHeadRows = 8;
 
-// Grid (ceil(H * nslices / 8), rows): block y = token row t (strided past 65535), warp w of the
-// block = (slice, head) pair blockIdx.x * 8 + w.
+// cos / sin of the two NeoX pairs (e & (rot/2 - 1)) of head elements e = 2l, 2l + 1
+__device__ __forceinline__ float4 rope_cs2(const float2* __restrict__ tab, int pos, int lane, int rot) {
+  const int half = rot / 2;
+  return *reinterpret_cast<const float4*>(tab + pos * half + ((2 * lane) & (half - 1)));
+}
+
+// Grid (ceil(H * nslices / 8), ceil(T / kHeadRows)); warp w of block x = (slice, head) pair 8 x + w.
 __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
                                      int tps, float eps, int rot, const float2* __restrict__ tab,
                                      __nv_bfloat16* __restrict__ out) {
@@ -123,69 +126,88 @@ __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int nco
   const int lane = threadIdx.x & 31;
   const int si = pair % nslices, h = pair / nslices;
   const HeadSlice sl = slices.s[si];
-  for (int t = blockIdx.y; t < T; t += gridDim.y) {
-  const long base = (long)t * ncols + sl.col + h * 64;
-  float a = y[base + lane], b = y[base + lane + 32];
-  if (sl.gamma) {
-    const float r = rsqrtf(warp_sum(a * a + b * b) / 64.f + eps);
-    if (lane == 0 && sl.rstd) sl.rstd[(long)t * H + h] = r;
-    a *= r * sl.gamma[lane];
-    b *= r * sl.gamma[lane + 32];
-  }
-  if (sl.rope) {
-    const int pos = t % tps;
-    if (rot == 32) {   // pairs (i, i + 16) for i < 16 live in lanes i and i ^ 16
-      const float pa = __shfl_xor_sync(0xffffffffu, a, 16);
-      float c, s;
-      rope_cs(tab, pos, lane & 15, rot, c, s);
-      a = lane < 16 ? a * c - pa * s : pa * s + a * c;
-    } else if (rot == 64) {   // pairs (i, i + 32) live in one lane
-      float c, s;
-      rope_cs(tab, pos, lane, rot, c, s);
-      const float na = a * c - b * s, nb = a * s + b * c;
-      a = na;
-      b = nb;
+  const int t0 = blockIdx.y * kHeadRows;
+  const float2 gm = sl.gamma ? reinterpret_cast<const float2*>(sl.gamma)[lane] : make_float2(1.f, 1.f);
+  float2 v[kHeadRows];
+#pragma unroll
+  for (int r = 0; r < kHeadRows; ++r)
+    v[r] = t0 + r < T ? reinterpret_cast<const float2*>(y + (long)(t0 + r) * ncols + sl.col + h * 64)[lane]
+                      : make_float2(0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < kHeadRows; ++r) {
+    const int t = t0 + r;
+    if (t >= T) break;
+    float a = v[r].x, b = v[r].y;
+    if (sl.gamma) {
+      const float rr = rsqrtf(warp_sum(a * a + b * b) / 64.f + eps);
+      if (lane == 0 && sl.rstd) sl.rstd[(long)t * H + h] = rr;
+      a *= rr * gm.x;
+      b *= rr * gm.y;
     }
-  }
-  out[base + lane] = __float2bfloat16_rn(a);
-  out[base + lane + 32] = __float2bfloat16_rn(b);
+    if (sl.rope && (rot == 32 || rot == 64)) {
+      const int px = rot == 32 ? 8 : 16;
+      const float pa = __shfl_xor_sync(0xffffffffu, a, px), pb = __shfl_xor_sync(0xffffffffu, b, px);
+      if (rot == 64 || lane < 16) {
+        const float4 cs = rope_cs2(tab, t % tps, lane, rot);
+        if ((lane & px) == 0) {   // first element of the pair: x cos - partner sin
+          a = a * cs.x - pa * cs.y;
+          b = b * cs.z - pb * cs.w;
+        } else {                  // second: partner sin + x cos
+          a = pa * cs.y + a * cs.x;
+          b = pb * cs.w + b * cs.z;
+        }
+      }
+    }
+    reinterpret_cast<__nv_bfloat162*>(out + (long)t * ncols + sl.col + h * 64)[lane] = __floats2bfloat162_rn(a, b);
   }
 }
 
-__global__ void head_prep_bwd_kernel(const float* __restrict__ g, long g_ld, const float* __restrict__ y, int T,
-                                     int ncols, int H, HeadSlice sl, int tps, int rot,
-                                     const float2* __restrict__ tab, float* __restrict__ dy) {
+__global__ void head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y, int T, int ncols, int H,
+                                     HeadSlice sl, int tps, int rot, const float2* __restrict__ tab, float* dy) {
   const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (h >= H) return;
   const int lane = threadIdx.x & 31;
-  for (int t = blockIdx.y; t < T; t += gridDim.y) {
-  float ga = g[(long)t * g_ld + h * 64 + lane], gb = g[(long)t * g_ld + h * 64 + lane + 32];
-  const long base = (long)t * ncols + sl.col + h * 64;
-  if (sl.rope) {   // inverse rotation of the gradient
-    const int pos = t % tps;
-    if (rot == 32) {
-      const float pa = __shfl_xor_sync(0xffffffffu, ga, 16);
-      float c, s;
-      rope_cs(tab, pos, lane & 15, rot, c, s);
-      ga = lane < 16 ? ga * c + pa * s : -pa * s + ga * c;
-    } else if (rot == 64) {
-      float c, s;
-      rope_cs(tab, pos, lane, rot, c, s);
-      const float na = ga * c + gb * s, nb = -ga * s + gb * c;
-      ga = na;
-      gb = nb;
+  const int t0 = blockIdx.y * kHeadRows;
+  const float2 gm = sl.gamma ? reinterpret_cast<const float2*>(sl.gamma)[lane] : make_float2(1.f, 1.f);
+  float2 gv[kHeadRows], yv[kHeadRows];
+  float rs[kHeadRows];
+#pragma unroll
+  for (int r = 0; r < kHeadRows; ++r) {
+    const int t = t0 + r;
+    const bool in = t < T;
+    gv[r] = in ? reinterpret_cast<const float2*>(g + (long)t * g_ld + h * 64)[lane] : make_float2(0.f, 0.f);
+    yv[r] = in && sl.gamma ? reinterpret_cast<const float2*>(y + (long)t * ncols + sl.col + h * 64)[lane]
+                           : make_float2(0.f, 0.f);
+    rs[r] = in && sl.gamma ? sl.rstd[(long)t * H + h] : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < kHeadRows; ++r) {
+    const int t = t0 + r;
+    if (t >= T) break;
+    float ga = gv[r].x, gb = gv[r].y;
+    if (sl.rope && (rot == 32 || rot == 64)) {   // inverse rotation of the gradient
+      const int px = rot == 32 ? 8 : 16;
+      const float pa = __shfl_xor_sync(0xffffffffu, ga, px), pb = __shfl_xor_sync(0xffffffffu, gb, px);
+      if (rot == 64 || lane < 16) {
+        const float4 cs = rope_cs2(tab, t % tps, lane, rot);
+        if ((lane & px) == 0) {
+          ga = ga * cs.x + pa * cs.y;
+          gb = gb * cs.z + pb * cs.w;
+        } else {
+          ga = -pa * cs.y + ga * cs.x;
+          gb = -pb * cs.w + gb * cs.z;
+        }
+      }
     }
-  }
-  if (sl.gamma) {
-    const float r = sl.rstd[(long)t * H + h];
-    const float na = y[base + lane] * r, nb = y[base + lane + 32] * r;
-    const float da = ga * sl.gamma[lane], db = gb * sl.gamma[lane + 32];
-    const float mean = warp_sum(da * na + db * nb) / 64.f;
-    ga = r * (da - na * mean);
-    gb = r * (db - nb * mean);
-  }
-  dy[base + lane] = ga;
-  dy[base + lane + 32] = gb;
+    if (sl.gamma) {
+      const float rr = rs[r];
+      const float na = yv[r].x * rr, nb = yv[r].y * rr;
+      const float da = ga * gm.x, db = gb * gm.y;
+      const float mean = warp_sum(da * na + db * nb) / 64.f;
+      ga = rr * (da - na * mean);
+      gb = rr * (db - nb * mean);
+    }
+    reinterpret_cast<float2*>(dy + (long)t * ncols + sl.col + h * 64)[lane] = make_float2(ga, gb);
   }
 }
 
@@ -375,7 +397,8 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   const float2* tab = nullptr;
   if (any_rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
-  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)(T < 65535 ? T : 65535));
+  if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
+  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
   head_prep_fwd_kernel<<<grid, 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
@@ -385,7 +408,8 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
-  const dim3 grid((unsigned)((H + 7) / 8), (unsigned)(T < 65535 ? T : 65535));
+  if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
+  const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
   head_prep_bwd_kernel<<<grid, 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
   return check_launch("head_prep_bwd", err);
 }

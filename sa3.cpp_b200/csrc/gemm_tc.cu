@@ -218,7 +218,7 @@ static int pick_bn(const Ctx* c, int M, int N, bool quant) {
 }
 
 int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
-  if (d.M <= 0 || d.N <= 0 || d.K < 0 || (d.K == 0 && !d.ext_a)) {
+  if (d.M <= 0 || d.N <= 0 || d.K < 0 || (d.K == 0 && !d.ext_at)) {
     err = "gemm: need M, N > 0 and K > 0";
     return 1;
   }
@@ -294,8 +294,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       }
     }
   }
-  if (d.ext_a) {
-    if (make_map(&tea, BF, d.ext_a, 64, d.M, 128, 64, kBM, SW, "ext A", err)) return 1;
+  if (d.ext_at) {
+    // u^T [16][ld_ext] read MN-major: boxes of 64 rows (M) x 16 (K)
+    if (make_map(&tea, BF, d.ext_at, d.M, 16, d.ld_ext * 2, 64, 16, SW, "ext A", err)) return 1;
     if (make_map(&teb, BF, d.ext_b, 64, d.N, 128, 64, bn, SW, "ext B", err)) return 1;
   } else {
     tea = ta;
@@ -305,7 +306,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
 
   GemmArgs a;
   a.M = d.M; a.N = d.N; a.K = d.K;
-  a.has_ext = d.ext_a ? 1 : 0;
+  a.has_ext = d.ext_at ? 1 : 0;
   a.col_scale = d.col_scale; a.col_bias = d.col_bias; a.alpha = d.alpha;
   a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
   a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans; a.bf_scale = d.bf_scale;
@@ -352,7 +353,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
         const long bld = d.bsrc == kB_BF16_KMAJOR ? d.ldb * 2 : d.w->in * 2;
         if (make_map(&tb2, BF, bptr, bk, d.N, bld, 64, bp / 2, SW, "B half", err)) return 1;
       }
-      if (d.ext_a) {
+      if (d.ext_at) {
         if (make_map(&teb2, BF, d.ext_b, 64, d.N, 128, 64, bp / 2, SW, "ext B half", err)) return 1;
       }
       if (bp == 192) return launch_pair<192, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err);

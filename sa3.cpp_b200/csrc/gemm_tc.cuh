@@ -61,6 +61,8 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128, kBK = 64;
+// the K = 16 extension's A tile: 128 rows of u^T as two 64 (M) x 16 (K) MN-major boxes
+constexpr int kExtABytes = 128 * 16 * 2;
 
 template <int BMODE>
 struct BModeTraits {
@@ -268,6 +270,45 @@ __device__ __forceinline__ void splitk_finish(const GemmArgs& args, int m0, int 
   }
 }
 
+// The same for a 16-wide output (N = 16): thread `tid` < rows owns one row and loads every
+// split's 16 partial sums (64 contiguous bytes each).  This path runs once per tile, so its code
+// is kept small (cold instruction fetches dominate otherwise): the finished row goes through the
+// thread's shared-memory slot `stage` (16 floats) and is written by one short loop.
+__device__ __forceinline__ void splitk_finish_rows16(const GemmArgs& args, int m0, int rows, int tid, float* stage) {
+  if (tid >= rows) return;
+  const long mn4 = (long)args.M * args.N / 4;
+  const int row = m0 + tid;
+  const float4* src = reinterpret_cast<const float4*>(args.partial + (long)row * args.N);
+  float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0, x2 = x0, x3 = x0;
+#pragma unroll 1
+  for (int sp = 0; sp < args.splits; ++sp) {
+    const float4* s = src + sp * mn4;
+    const float4 p0 = __ldcg(s), p1 = __ldcg(s + 1), p2 = __ldcg(s + 2), p3 = __ldcg(s + 3);
+    x0.x += p0.x; x0.y += p0.y; x0.z += p0.z; x0.w += p0.w;
+    x1.x += p1.x; x1.y += p1.y; x1.z += p1.z; x1.w += p1.w;
+    x2.x += p2.x; x2.y += p2.y; x2.z += p2.z; x2.w += p2.w;
+    x3.x += p3.x; x3.y += p3.y; x3.z += p3.z; x3.w += p3.w;
+  }
+  float4* st = reinterpret_cast<float4*>(stage);
+  st[0] = x0; st[1] = x1; st[2] = x2; st[3] = x3;
+#pragma unroll 1
+  for (int col = 0; col < 16; ++col) {
+    float v = stage[col] * args.alpha;
+    if (args.col_scale) v *= args.col_scale[col];
+    if (args.col_bias) v += args.col_bias[col];
+    if (args.out) {
+      float* dst = args.out_trans ? args.out + (long)col * args.ldo + row : args.out + (long)row * args.ldo + col;
+      *dst = args.accumulate ? *dst + v : v;
+    }
+    if (args.out_bf) {
+      __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)col * args.ldo_bf + row
+                                             : args.out_bf + (long)row * args.ldo_bf + col;
+      *dst = __float2bfloat16_rn(v * args.bf_scale);
+    }
+    if (args.out_bf_t) args.out_bf_t[(long)col * args.ldo_bf_t + row] = __float2bfloat16_rn(v);
+  }
+}
+
 // ------------------------------------------------------------------ the kernel
 // Persistent: gridDim.x CTAs walk the work items blockIdx.x, blockIdx.x + gridDim.x, ...; an item
 // is an output tile t (m-tile t % tiles_m, n-tile t / tiles_m, so co-resident CTAs share B
@@ -279,7 +320,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                    const __grid_constant__ CUtensorMap tm_bs, const __grid_constant__ CUtensorMap tm_ea,
                    const __grid_constant__ CUtensorMap tm_eb, const __grid_constant__ CUtensorMap tm_out,
-                   const GemmArgs args) {
+                   const __grid_constant__ GemmArgs args) {
   using T = BModeTraits<BMODE>;
   using L = GemmSmem<BN, STAGES, BMODE>;
   using R = GemmRoles<BMODE>;
@@ -402,8 +443,10 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
               tma_load_2d(sc, &tm_bs, &full[s], k0, n0 / 32);
             }
           } else {
-            mbar_arrive_expect_tx(&full[s], (uint32_t)(L::A_BYTES + L::B_BYTES));
-            tma_load_2d(a_st, &tm_ea, &full[s], 0, m0);
+            // K = 16 extension: u^T rows m0 .. m0 + 127 as two MN-major 64 x 16 boxes, B ext tile
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(kExtABytes + L::B_BYTES));
+            tma_load_2d(a_st, &tm_ea, &full[s], m0, 0);
+            tma_load_2d(a_st + kExtABytes / 2, &tm_ea, &full[s], m0 + 64, 0);
             tma_load_2d(b_st, &tm_eb, &full[s], 0, n0);
           }
         }
@@ -417,13 +460,13 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     // 2^18, so the field never carries into the next one).
     const WaiterW<> wt{abort_flag, args.err};
     const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
-    const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 0, 0);
+    const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 1, 0);   // A = u^T read MN-major
     const uint64_t adesc0 = A_MN ? make_sdesc(smem_u32(smem + L::OFF_A), 8192, 1024)
                                  : make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
     const uint64_t bdesc0 = T::mn ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
                                   : make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
     const uint64_t bdesc0_k = make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
-    const uint64_t adesc0_k = make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
+    const uint64_t adesc0_ext = make_sdesc(smem_u32(smem + L::OFF_A), kExtABytes / 2, 1024);
     constexpr uint32_t A_KSTEP = A_MN ? 2048 >> 4 : 32 >> 4;
     constexpr uint32_t B_KSTEP = T::mn ? 2048 >> 4 : 32 >> 4;
     int it = 0, ti = 0;
@@ -449,7 +492,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             umma_bf16_w(d_tmem, adesc0 + aoff + kk * A_KSTEP, bdesc0 + boff + kk * B_KSTEP, idesc,
                         (kb > 0 || kk > 0) ? 1u : 0u);
         } else {
-          umma_bf16_w(d_tmem, adesc0_k + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
+          umma_bf16_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
         }
         umma_commit_w(&empty[s]);
       }
@@ -555,6 +598,16 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             if (args.out_bf_t) args.out_bf_t[(long)(nb + j) * args.ldo_bf_t + myrow] = __float2bfloat16_rn(f[j]);
           }
         }
+        if (BN == 16 && split_out && args.N == 16) {
+          // narrow tile: each lane stores its row's 16 partial sums as four 16-byte pieces
+          if (myrow < args.M) {
+            float4* dst = reinterpret_cast<float4*>(args.partial + (long)(item / ntiles) * args.M * args.N +
+                                                    (long)myrow * args.N + nb);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dst[c] = make_float4(f[4 * c], f[4 * c + 1], f[4 * c + 2], f[4 * c + 3]);
+          }
+          continue;
+        }
         if (split_out || (args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
           float* st32 = reinterpret_cast<float*>(stg);     // 32 x 32 f32, XOR-swizzled columns
 #pragma unroll
@@ -595,8 +648,11 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         named_bar(1, 32 * R::EPI_WARPS);
         if (*last_split) {
           __threadfence();
-          splitk_finish(args, m0, n0, min(kBM, args.M - m0), min(BN, args.N - n0), threadIdx.x - 64,
-                        32 * R::EPI_WARPS);
+          if (BN == 16 && args.N == 16)
+            splitk_finish_rows16(args, m0, min(kBM, args.M - m0), threadIdx.x - 64,
+                                 reinterpret_cast<float*>(stg) + 16 * lane);
+          else splitk_finish(args, m0, n0, min(kBM, args.M - m0), min(BN, args.N - n0), threadIdx.x - 64,
+                             32 * R::EPI_WARPS);
         }
       }
       tc_fence_before();

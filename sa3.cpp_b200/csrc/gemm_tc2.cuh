@@ -123,7 +123,7 @@ template <int BN, int STAGES, int BMODE>
 __global__ void __launch_bounds__(kPairThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                     const __grid_constant__ CUtensorMap tm_ea, const __grid_constant__ CUtensorMap tm_eb,
-                    const __grid_constant__ CUtensorMap tm_out, const GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ GemmArgs args) {
   using L = Gemm2Smem<BN, STAGES>;
   constexpr bool BMN = BMODE == 1;
   constexpr int EPI_WARPS = kPairEpiWarps;
@@ -209,7 +209,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           uint8_t* a_st = smem + L::OFF_A + s * L::A_BYTES;
           uint8_t* b_st = smem + L::OFF_B + s * L::B_BYTES;
           const uint32_t fb = full0 + (uint32_t)(s * 8);
-          if (leader) mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)(L::A_BYTES + L::B_BYTES));
+          if (leader)
+            mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)((kb < nkb ? L::A_BYTES : kExtABytes) + L::B_BYTES));
           if (kb < nkb) {
             const int k0 = kb * kBK;
             tma_load_2d_pair(a_st, &tm_a, fb, k0, m0);
@@ -220,7 +221,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               for (int j = 0; j < L::BH / 64; ++j) tma_load_2d_pair(b_st + j * 8192, &tm_b, fb, n0 + 64 * j, k0);
             }
           } else {
-            tma_load_2d_pair(a_st, &tm_ea, fb, 0, m0);
+            tma_load_2d_pair(a_st, &tm_ea, fb, m0, 0);               // u^T, MN-major
+            tma_load_2d_pair(a_st + kExtABytes / 2, &tm_ea, fb, m0 + 64, 0);
             tma_load_2d_pair(b_st, &tm_eb, fb, 0, n0);
           }
         }
@@ -232,11 +234,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (leader) {
       const WaiterW<true> wt{abort_flag, args.err};
       const uint32_t idesc = make_idesc_bf16(PM, BN, 0, BMN ? 1 : 0);
-      const uint32_t idesc_ext = make_idesc_bf16(PM, BN, 0, 0);
+      const uint32_t idesc_ext = make_idesc_bf16(PM, BN, 1, 0);   // A = u^T read MN-major
       const uint64_t adesc0 = make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
       const uint64_t bdesc0 = BMN ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
                                   : make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
       const uint64_t bdesc0_k = make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
+      const uint64_t adesc0_ext = make_sdesc(smem_u32(smem + L::OFF_A), kExtABytes / 2, 1024);
       constexpr uint32_t B_KSTEP = BMN ? 2048 >> 4 : 32 >> 4;
       int it = 0, ti = 0;
       bool ok = true;
@@ -258,7 +261,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               umma_bf16_pair_w(d_tmem, adesc0 + aoff + kk * 2u, bdesc0 + boff + kk * B_KSTEP, idesc,
                                (kb > 0 || kk > 0) ? 1u : 0u);
           } else {
-            umma_bf16_pair_w(d_tmem, adesc0 + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
+            umma_bf16_pair_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
           }
           umma_commit_pair_w(&empty[s]);
         }

@@ -1,7 +1,7 @@
 // linear.cu -- forward and backward of the adapted frozen-base linear over the tcgen05 engine.
 //
 // Forward (src/dit.h:106-147):
-//   u = x A^T                               rank-16 GEMM, written as bf16 s u [M][64] and u^T
+//   u = x A^T                               rank-16 GEMM, written as bf16 u^T [16][M]
 //   y = g * (x W^T  (+)  (s u) B^T) + bias  one GEMM: the LoRA term is a K = 16 extension of the
 //                                           base MMA chain; g (DoRA) and bias in the epilogue
 // Backward (what ggml_build_backward_expand derives for those ops, src/train_ckpt.h:400):
@@ -57,20 +57,19 @@ int adapter_dora_p(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
 }
 
 int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
-  if (k_prep_adapter(c, p.A, p.B, p.rank, p.in, p.out, p.a_bf, p.at_x, p.b_x, p.bt_bf, err)) return 1;
+  if (k_prep_adapter(c, p.A, p.B, p.rank, p.s, p.in, p.out, p.a_bf, p.at_x, p.b_x, p.bt_bf, err)) return 1;
   if (!p.dora()) return 0;
   if (adapter_dora_p(c, w, p, err)) return 1;
   if (k_aat(c, p.A, p.rank, p.in, p.aat, err)) return 1;
   return k_dora_norm(c, p.pt, p.B, p.rank, p.out, p.aat, p.bns, p.m, p.s, p.nsq, p.g, err);
 }
 
-int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ext_u,
-           __nv_bfloat16* ut, int64_t ut_ld, std::string& err) {
-  GemmDesc g;   // u = x A^T  [M][16]: ext_u = bf16(s u) row-major [M][64], ut = bf16(u) as [16][ut_ld]
+int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ut,
+           int64_t ut_ld, std::string& err) {
+  GemmDesc g;   // u = x A^T  [M][16], written as ut = bf16(u)^T [16][ut_ld]
   g.M = (int)M; g.N = 16; g.K = (int)in;
   g.a = x_bf; g.lda = in;
   g.bsrc = kB_BF16_KMAJOR; g.b = ad.a_bf; g.ldb = in;
-  g.out_bf = ext_u; g.ldo_bf = 64; g.bf_scale = ad.s;
   g.out_bf_t = ut; g.ldo_bf_t = ut_ld;
   g.bn = 16;
   g.name = "lora.u";
@@ -80,12 +79,12 @@ int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const Adapt
 int linear_forward(Ctx* c, const LinearFwd& f, std::string& err) {
   const Weight* w = f.w;
   const AdapterPrep* ad = f.ad;
-  if (ad && lora_u(c, f.x_bf, f.M, w->in, *ad, f.ext_u, f.ut, f.ut_ld, err)) return 1;
+  if (ad && lora_u(c, f.x_bf, f.M, w->in, *ad, f.ut, f.ut_ld, err)) return 1;
   GemmDesc g;   // y = g * (x W^T + s u B^T) + bias
   g.M = (int)f.M; g.N = (int)w->out; g.K = (int)w->in;
   g.a = f.x_bf; g.lda = w->in;
   g.bsrc = kB_WEIGHT_NT; g.w = w;
-  if (ad) { g.ext_a = f.ext_u; g.ext_b = ad->b_x; }
+  if (ad) { g.ext_at = f.ut; g.ld_ext = f.ut_ld; g.ext_b = ad->b_x; }
   g.col_scale = (ad && ad->dora()) ? ad->g : nullptr;
   g.col_bias = f.bias;
   g.out = f.y; g.ldo = w->out;
@@ -108,12 +107,11 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
       return 1;
   }
   if (ad) {
-    GemmDesc g;   // du = s dz B  [M][16]: ext_du row-major [M][64] and dut [16][ut_ld], both bf16
+    GemmDesc g;   // du = s dz B  [M][16], written as dut = bf16(du)^T [16][ut_ld]
     g.M = (int)b.M; g.N = 16; g.K = (int)out;
     g.a = b.dz; g.lda = out;
     g.bsrc = kB_BF16_KMAJOR; g.b = ad->bt_bf; g.ldb = out;
     g.alpha = ad->s;
-    g.out_bf = b.ext_du; g.ldo_bf = 64;
     g.out_bf_t = b.dut; g.ldo_bf_t = b.ut_ld;
     g.bn = 16;
     g.name = "lora.du";
@@ -124,7 +122,7 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
     g.M = (int)b.M; g.N = (int)in; g.K = (int)out;
     g.a = b.dz; g.lda = out;
     g.bsrc = kB_WEIGHT_TN; g.w = w;
-    if (ad) { g.ext_a = b.ext_du; g.ext_b = ad->at_x; }
+    if (ad) { g.ext_at = b.dut; g.ld_ext = b.ut_ld; g.ext_b = ad->at_x; }
     g.out = b.dx; g.ldo = in; g.accumulate = b.dx_accumulate;
     g.out_bf = b.dx_bf; g.ldo_bf = in;
     g.name = "linear.dx";

@@ -43,15 +43,14 @@ struct LinearFwd {
   int64_t M = 0;
   float* y = nullptr;                  // [M][out] f32 output (nullable)
   __nv_bfloat16* y_bf = nullptr;       // [M][out] bf16 output (nullable)
-  // adapter scratch: ext_u [M][64] bf16 (s u), ut [16][ut_ld] bf16 (u^T, kept for backward)
-  __nv_bfloat16* ext_u = nullptr;
+  // adapter scratch: ut [16][ut_ld] bf16 (u^T: the K = 16 extension operand, kept for backward)
   __nv_bfloat16* ut = nullptr;
   int64_t ut_ld = 0;
 };
 int linear_forward(Ctx* c, const LinearFwd& f, std::string& err);
-// u = x A^T of an adapter: ext_u = bf16(s u) [M][64] (columns 0..15), ut = bf16(u) [16][ut_ld]
-int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ext_u,
-           __nv_bfloat16* ut, int64_t ut_ld, std::string& err);
+// u = x A^T of an adapter, written as ut = bf16(u)^T [16][ut_ld]
+int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ut,
+           int64_t ut_ld, std::string& err);
 
 struct LinearBwd {
   const Weight* w = nullptr;
@@ -73,11 +72,10 @@ struct LinearBwd {
   float* dB = nullptr;                 // [out][rank]
   float* dm = nullptr;                 // [out] (dora)
   int grad_accumulate = 0;
-  // scratch: dz [M][out] bf16, dg [out], ext_du [M][64] bf16, dut [16][ut_ld] bf16,
+  // scratch: dz [M][out] bf16, dg [out], dut [16][ut_ld] bf16,
   // cb [16][out] bf16, c3 [256]
   __nv_bfloat16* dz = nullptr;
   float* dg = nullptr;
-  __nv_bfloat16* ext_du = nullptr;
   __nv_bfloat16* dut = nullptr;
   __nv_bfloat16* cb = nullptr;
   float* c3 = nullptr;

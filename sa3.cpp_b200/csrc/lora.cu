@@ -32,9 +32,9 @@ __global__ void cvt_bf16_kernel(const float* __restrict__ src, int64_t n, __nv_b
 // Adapter operand forms.  A f32 [rank][in], B f32 [out][rank].
 //   a_bf  bf16 [16][in]    (rows >= rank zero)      B operand of u = x A^T, A operand of W A^T
 //   at_x  bf16 [in][64]    A^T in columns 0..15     K-extension B operand of dx
-//   b_x   bf16 [out][64]   B in columns 0..15       K-extension B operand of y
+//   b_x   bf16 [out][64]   s B in columns 0..15     K-extension B operand of y
 //   bt_bf bf16 [16][out]   B^T                      B operand of du = dz B
-__global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __restrict__ B, int rank,
+__global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __restrict__ B, int rank, float s,
                                     int64_t in, int64_t out, __nv_bfloat16* __restrict__ a_bf,
                                     __nv_bfloat16* __restrict__ at_x, __nv_bfloat16* __restrict__ b_x,
                                     __nv_bfloat16* __restrict__ bt_bf) {
@@ -51,7 +51,7 @@ __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __
     const int64_t o = k / 64;
     const int c = (int)(k % 64);
     const float b = (c < rank) ? B[o * rank + c] : 0.f;
-    b_x[k] = __float2bfloat16_rn(b);
+    b_x[k] = __float2bfloat16_rn(s * b);
     if (c < R) bt_bf[(int64_t)c * out + o] = __float2bfloat16_rn(b);
   }
 }
@@ -129,7 +129,8 @@ __device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4
   *reinterpret_cast<uint2*>(dz) = pk;
 }
 
-// dy = gx * gate[sample] (the gate backward of src/dit.h:186-193)
+// dy = gx * gate[sample] (the gate backward of src/dit.h:186-193).  Rows are processed four at a
+// time with all their loads issued first.
 __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride,
                                    int T, int D, int tps, const float* __restrict__ y, const float* __restrict__ bias,
                                    const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
@@ -150,18 +151,28 @@ __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __
     }
   }
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int t = t0; t < t1; ++t) {
-    const long e = (long)t * D + c0;
-    const float4 gt = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + c0);
-    const float4 a = *reinterpret_cast<const float4*>(gx + e);
-    const float dy[4] = {a.x * gt.x, a.y * gt.y, a.z * gt.z, a.w * gt.w};
-    dz_store4(dz + e, dy, gv, dora);
-    if (dora) {
-      const float4 yv = *reinterpret_cast<const float4*>(y + e);
-      acc[0] = fmaf(dy[0], (yv.x - bv[0]) * inv[0], acc[0]);
-      acc[1] = fmaf(dy[1], (yv.y - bv[1]) * inv[1], acc[1]);
-      acc[2] = fmaf(dy[2], (yv.z - bv[2]) * inv[2], acc[2]);
-      acc[3] = fmaf(dy[3], (yv.w - bv[3]) * inv[3], acc[3]);
+  for (int tb = t0; tb < t1; tb += 4) {
+    float4 gt[4], av[4], yv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = min(tb + u, t1 - 1);          // rows past the end repeat the last (not stored)
+      const long e = (long)t * D + c0;
+      gt[u] = *reinterpret_cast<const float4*>(gate + (long)(t / tps) * gstride + c0);
+      av[u] = *reinterpret_cast<const float4*>(gx + e);
+      if (dora) yv[u] = *reinterpret_cast<const float4*>(y + e);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (tb + u >= t1) break;
+      const long e = (long)(tb + u) * D + c0;
+      const float dy[4] = {av[u].x * gt[u].x, av[u].y * gt[u].y, av[u].z * gt[u].z, av[u].w * gt[u].w};
+      dz_store4(dz + e, dy, gv, dora);
+      if (dora) {
+        acc[0] = fmaf(dy[0], (yv[u].x - bv[0]) * inv[0], acc[0]);
+        acc[1] = fmaf(dy[1], (yv[u].y - bv[1]) * inv[1], acc[1]);
+        acc[2] = fmaf(dy[2], (yv[u].z - bv[2]) * inv[2], acc[2]);
+        acc[3] = fmaf(dy[3], (yv[u].w - bv[3]) * inv[3], acc[3]);
+      }
     }
   }
   if (dora) {
@@ -192,11 +203,21 @@ __global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const float* 
     }
   }
   float accv[4] = {0.f, 0.f, 0.f, 0.f}, accg[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int t = t0; t < t1; ++t) {
-    const float* fr = f + (long)t * 2 * I;
-    const float4 v = *reinterpret_cast<const float4*>(fr + j);
-    const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
-    const float4 d = *reinterpret_cast<const float4*>(da + (long)t * I + j);
+  for (int tb = t0; tb < t1; tb += 2) {
+    float4 v2[2], g2[2], d2[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {                    // both rows' loads first
+      const int t = min(tb + u, t1 - 1);
+      const float* fr = f + (long)t * 2 * I;
+      v2[u] = *reinterpret_cast<const float4*>(fr + j);
+      g2[u] = *reinterpret_cast<const float4*>(fr + I + j);
+      d2[u] = *reinterpret_cast<const float4*>(da + (long)t * I + j);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+    const int t = tb + u;
+    if (t >= t1) break;
+    const float4 v = v2[u], gl = g2[u], d = d2[u];
     const float vv[4] = {v.x, v.y, v.z, v.w}, gg[4] = {gl.x, gl.y, gl.z, gl.w}, dd[4] = {d.x, d.y, d.z, d.w};
     float dv[4], dgl[4];
 #pragma unroll
@@ -214,6 +235,7 @@ __global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const float* 
         accv[e] = fmaf(dv[e], (vv[e] - bvv[e]) / gvv[e], accv[e]);
         accg[e] = fmaf(dgl[e], (gg[e] - bgg[e]) / ggg[e], accg[e]);
       }
+    }
     }
   }
   if (dora) {
@@ -242,7 +264,7 @@ __global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
   for (int k = t0; k < nout; k += stride) {
     const int o = k >> 6, c = k & 63;
     const float b = (c < d.rank) ? d.B[(int64_t)o * d.rank + c] : 0.f;
-    d.b_x[k] = __float2bfloat16_rn(b);
+    d.b_x[k] = __float2bfloat16_rn(d.s * b);
     if (c < R) d.bt_bf[(int64_t)c * d.out + o] = __float2bfloat16_rn(b);
   }
 }
@@ -454,11 +476,12 @@ int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::str
   return check_launch("cvt_bf16", err);
 }
 
-int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
+int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, float s, int64_t in, int64_t out,
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err) {
   ProfScope prof_(c, "prep_adapter");
-  prep_adapter_kernel<<<grid1d((in + out) * 64, 256), 256, 0, c->stream>>>(A, B, rank, in, out, a_bf, at_x, b_x, bt_bf);
+  prep_adapter_kernel<<<grid1d((in + out) * 64, 256), 256, 0, c->stream>>>(A, B, rank, s, in, out, a_bf, at_x, b_x,
+                                                                             bt_bf);
   return check_launch("prep_adapter", err);
 }
 

@@ -32,7 +32,7 @@ int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::
 // grouped DoRA backward (dm, dB, cb, c3 from dg) and the dA += 2 c3 A term, over n adapters
 int k_dora_bwd_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
 int k_dora_da_c3_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
-int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, int64_t in, int64_t out,
+int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, float s, int64_t in, int64_t out,
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err);
 int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err);

@@ -124,8 +124,10 @@ struct GemmDesc {
   const __nv_bfloat16* b = nullptr;
   long ldb = 0;
   const Weight* w = nullptr;
-  // K = 16 extension: ext_a bf16 [M][64], ext_b bf16 [N][64] (columns 16..63 are not read)
-  const __nv_bfloat16* ext_a = nullptr;
+  // K = 16 extension: ext_at bf16 [16][ld_ext] (the rank-16 left factor transposed, read
+  // MN-major), ext_b bf16 [N][64] (columns 16..63 are not read)
+  const __nv_bfloat16* ext_at = nullptr;
+  long ld_ext = 0;
   const __nv_bfloat16* ext_b = nullptr;
   // epilogue
   const float* col_scale = nullptr;

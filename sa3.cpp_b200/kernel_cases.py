@@ -3,10 +3,11 @@ few times through the C ABI, so that a profiler (ncu -k regex:gemm_tc -c 1) sees
 launches of one GEMM on inputs larger than L2 and a few hundred MB on the device.
 
     python sa3.cpp_b200/kernel_cases.py gemm --m 4352 --n 1536 --k 1536 [--dx] [--qtype q8_0]
-        [--pair 0|1] [--tile-n 0|128|192|256] [--reps 3] [--time]
+        [--pair 0|1|2] [--tile-n 0|128|192|256] [--adapter] [--reps 3] [--time]
 
 --dx runs the input-gradient GEMM dx[m][k] = dy[m][n] . W[n][k] of a linear with in = k,
 out = n (the weight is used transposed); the default is the forward y = x W^T + 0.
+--adapter adds a rank-16 LoRA adapter (the forward then also runs u = x A^T).
 --time prints the CUDA-event time per launch (not to be used under a profiler)."""
 import argparse
 import os
@@ -33,13 +34,20 @@ def gemm_case(a):
     dev = torch.device("cuda", 0)
     x = torch.randn(a.m, a.k, device=dev)
     y = torch.empty(a.m, a.n, device=dev)
+    ad = None
+    if a.adapter:
+        A = torch.randn(16, a.k, device=dev) * 0.02
+        Bm = torch.randn(a.n, 16, device=dev) * 0.02
+        ad = ctx.adapter(A, Bm, 1.0)
     if a.dx:
         dy = torch.randn(a.m, a.n, device=dev)
         dx = torch.empty(a.m, a.k, device=dev)
-        run = lambda: ctx.linear_bwd(w, x, y, dy, dx)
+        gA = torch.zeros(16, a.k, device=dev) if ad else None
+        gB = torch.zeros(a.n, 16, device=dev) if ad else None
+        run = lambda: ctx.linear_bwd(w, x, y, dy, dx, ad=ad, dA=gA, dB=gB)
         flops = 2.0 * a.m * a.n * a.k
     else:
-        run = lambda: ctx.linear_fwd(w, x, y)
+        run = lambda: ctx.linear_fwd(w, x, y, ad=ad)
         flops = 2.0 * a.m * a.n * a.k
     for _ in range(a.warmup):
         run()
@@ -55,6 +63,9 @@ def gemm_case(a):
         n, ms = pr[name]
         print(f"{'dx' if a.dx else 'fwd'} {a.m}x{a.n}x{a.k} {a.qtype} pair{a.pair} bn{a.tile_n}: "
               f"{ms / n * 1e3:.1f} us/launch, {flops * n / (ms / 1e3) / 1e12:.1f} TFLOP/s")
+        for other, (n2, ms2) in sorted(pr.items()):
+            if other != name:
+                print(f"    {other}: {n2 // a.reps} launch(es) per call, {ms2 / a.reps * 1e3:.1f} us per call")
     w.free()
     ctx.close()
 
@@ -70,6 +81,7 @@ def main():
     gp.add_argument("--qtype", default="f32", choices=["f32", "q8_0", "q4_k"])
     gp.add_argument("--pair", type=int, default=1)
     gp.add_argument("--tile-n", type=int, default=0)
+    gp.add_argument("--adapter", action="store_true")
     gp.add_argument("--warmup", type=int, default=2)
     gp.add_argument("--reps", type=int, default=3)
     gp.add_argument("--time", action="store_true")
