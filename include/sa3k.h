@@ -68,6 +68,11 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       dS fed back from TMEM); 0: the mma.sync kernels.  Both compute in bf16 with f32
  *       accumulation; results agree to rounding. */
 #define SA3K_OPT_ATTN_TC 5
+/* SA3K_OPT_PDL  1 (default): kernels launched outside a stream capture use programmatic
+ *       dependent launch, so the next kernel of the stream is scheduled while the previous one
+ *       drains (each kernel waits for its predecessor's results before reading them; captured
+ *       graphs keep plain edges, which replay faster); 0: plain stream order always. */
+#define SA3K_OPT_PDL 6
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded

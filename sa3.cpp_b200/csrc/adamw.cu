@@ -18,6 +18,7 @@ namespace sa3k {
 // acc += sum_i (g_i * inv)^2 in f64, where g_i * inv is rounded to f32 first as the
 // reference averages in place before it accumulates (src/train_loop.h:150-160).
 __global__ void sumsq_kernel(const float* __restrict__ g, int64_t n, float inv, double* __restrict__ acc) {
+  pdl_prologue();
   double s = 0.0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -40,6 +41,7 @@ __global__ void sumsq_kernel(const float* __restrict__ g, int64_t n, float inv, 
 // scales[0] = 1/count, scales[1] = clip factor (1 when no clipping applies), norm_out = norm.
 __global__ void clip_scale_kernel(const double* __restrict__ sumsq, float grad_clip, float inv_count,
                                   float* __restrict__ scales, double* __restrict__ norm_out) {
+  pdl_prologue();
   const double norm = sqrt(*sumsq);
   if (norm_out) *norm_out = norm;
   scales[0] = inv_count;
@@ -49,6 +51,7 @@ __global__ void clip_scale_kernel(const double* __restrict__ sumsq, float grad_c
 __global__ void adamw_kernel(float* __restrict__ p, const float* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, int64_t n, float lr, float b1, float b2, float eps,
                              float wd, float b1c, float b2c, const float* __restrict__ scales) {
+  pdl_prologue();
   const float inv = scales ? scales[0] : 1.0f;
   const float clip = scales ? scales[1] : 1.0f;
   const float omb1 = 1.0f - b1, omb2 = 1.0f - b2;
@@ -77,21 +80,21 @@ static unsigned blocks_for(int64_t n) {
 
 int k_sumsq(Ctx* c, const float* g, int64_t n, float inv, double* acc, std::string& err) {
   ProfScope prof_(c, "sumsq");
-  sumsq_kernel<<<blocks_for(n), 256, 0, c->stream>>>(g, n, inv, acc);
+  launch_pdl(c, sumsq_kernel, blocks_for(n), 256, 0, g, n, inv, acc);
   return check_launch("sumsq", err);
 }
 
 int k_clip_scale(Ctx* c, const double* sumsq, float grad_clip, float inv_count, float* scales,
                  double* norm_out, std::string& err) {
   ProfScope prof_(c, "clip_scale");
-  clip_scale_kernel<<<1, 1, 0, c->stream>>>(sumsq, grad_clip, inv_count, scales, norm_out);
+  launch_pdl(c, clip_scale_kernel, 1, 1, 0, sumsq, grad_clip, inv_count, scales, norm_out);
   return check_launch("clip_scale", err);
 }
 
 int k_adamw(Ctx* c, float* p, const float* g, float* m, float* v, int64_t n, float lr, float b1, float b2,
             float eps, float wd, float b1c, float b2c, const float* scales, std::string& err) {
   ProfScope prof_(c, "adamw");
-  adamw_kernel<<<blocks_for(n), 256, 0, c->stream>>>(p, g, m, v, n, lr, b1, b2, eps, wd, b1c, b2c, scales);
+  launch_pdl(c, adamw_kernel, blocks_for(n), 256, 0, p, g, m, v, n, lr, b1, b2, eps, wd, b1c, b2c, scales);
   return check_launch("adamw", err);
 }
 

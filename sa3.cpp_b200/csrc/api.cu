@@ -255,6 +255,7 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
       ctx->c.gemm_pair = (int)value;
       return 0;
     case SA3K_OPT_ATTN_TC: ctx->c.attn_tc = value != 0; return 0;
+    case SA3K_OPT_PDL: ctx->c.pdl = value != 0; return 0;
     default: return fill_err(err, err_len, "unknown option");
   }
 }

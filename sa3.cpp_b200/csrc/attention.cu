@@ -137,6 +137,7 @@ __device__ __forceinline__ void key_range(int q0, int Sk, int window, int& kt0, 
 
 // ---------------------------------------------------------------------------------- forward
 __global__ void __launch_bounds__(NT) attn_fwd_kernel(const AttnArgs p) {
+  pdl_prologue();
   extern __shared__ __align__(1024) uint8_t sm[];    // Q, K[2], V[2]
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
@@ -235,6 +236,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const AttnArgs p) {
 
 // D[bh][q] = sum_d dO[b,h,q,d] * O[b,h,q,d]  (one warp per (bh, q) row)
 __global__ void attn_bwd_pre_kernel(const AttnArgs p) {
+  pdl_prologue();
   const long row = (long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   const long nrows = (long)p.B * p.H * p.Sq;
   if (row >= nrows) return;
@@ -250,6 +252,7 @@ __global__ void attn_bwd_pre_kernel(const AttnArgs p) {
 
 // ---------------------------------------------------------------------------------- dq pass
 __global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(const AttnArgs p) {
+  pdl_prologue();
   extern __shared__ __align__(1024) uint8_t sm[];    // Q, dO, K[2], V[2]
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t4 = lane & 3;
@@ -326,6 +329,7 @@ __global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(const AttnArgs p) {
 
 // ---------------------------------------------------------------------------------- dkdv pass
 __global__ void __launch_bounds__(NT) attn_bwd_dkdv_kernel(const AttnArgs p) {
+  pdl_prologue();
   extern __shared__ __align__(1024) uint8_t sm[];    // K, V, Q[2], dO[2], then lse / D [2][64]
   float (*s_lse)[TQ] = reinterpret_cast<float (*)[TQ]>(sm + 8192 * 6);
   float (*s_D)[TQ] = reinterpret_cast<float (*)[TQ]>(sm + 8192 * 6 + 2 * TQ * 4);
@@ -431,7 +435,7 @@ int attn_forward(Ctx* c, const AttnArgs& a, std::string& err) {
   if (set_attrs(err)) return 1;
   ProfScope prof_(c, "attn.fwd");
   dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));
-  attn_fwd_kernel<<<grid, NT, kSmemFwd, c->stream>>>(a);
+  launch_pdl(c, attn_fwd_kernel, grid, NT, kSmemFwd, a);
   return check_launch("attn fwd", err);
 }
 
@@ -443,19 +447,19 @@ int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err) {
   {
     ProfScope prof_(c, "attn.bwd_pre");
     const long rows = (long)a.B * a.H * a.Sq;
-    attn_bwd_pre_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, c->stream>>>(a);
+    launch_pdl(c, attn_bwd_pre_kernel, (unsigned)((rows + 7) / 8), 256, 0, a);
     if (check_launch("attn bwd pre", err)) return 1;
   }
   {
     ProfScope prof_(c, "attn.bwd_dq");
     dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));
-    attn_bwd_dq_kernel<<<grid, NT, kSmemDq, c->stream>>>(a);
+    launch_pdl(c, attn_bwd_dq_kernel, grid, NT, kSmemDq, a);
     if (check_launch("attn bwd dq", err)) return 1;
   }
   if (want_dkdv) {
     ProfScope prof_(c, "attn.bwd_dkdv");
     dim3 grid((unsigned)((a.Sk + TK - 1) / TK), (unsigned)(a.B * a.H));
-    attn_bwd_dkdv_kernel<<<grid, NT, kSmemDkdv, c->stream>>>(a);
+    launch_pdl(c, attn_bwd_dkdv_kernel, grid, NT, kSmemDkdv, a);
     if (check_launch("attn bwd dkdv", err)) return 1;
   }
   return 0;

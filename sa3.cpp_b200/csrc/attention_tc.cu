@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     attn_tc_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                        const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + 32768;
@@ -258,6 +259,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
   const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
@@ -472,6 +474,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                       const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_dq,
                       const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQd = smem;                  // [2 items][Q 16 KB | dO 16 KB | O 16 KB]
   uint8_t* sKV = smem + 98304;
@@ -529,6 +532,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
   const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
 
@@ -776,6 +780,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
                         const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
                         const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = smem + 16384;
@@ -824,6 +829,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
   const uint32_t tV = tbase + 384, tK = tbase + 448;
   const Waiter wait{abort_flag, a.err};     // single-thread roles (the TMA producer)
   const WaiterW<> waitw{abort_flag, a.err};   // whole-warp roles (MMA issue, softmax)
@@ -1073,7 +1079,7 @@ int attn_tc_forward(Ctx* c, const AttnArgs& p, std::string& err) {
     return 1;
   ProfScope prof_(c, "attn.fwd");
   dim3 grid((unsigned)((p.Sq + 255) / 256), (unsigned)(p.B * p.H));
-  attn_tc_fwd_kernel<<<grid, kThreadsTC, smem_req(F_SMEM), c->stream>>>(mq, mk, mv, a);
+  launch_pdl(c, attn_tc_fwd_kernel, grid, kThreadsTC, smem_req(F_SMEM), mq, mk, mv, a);
   return check_launch("attn tc fwd", err);
 }
 
@@ -1094,7 +1100,7 @@ int attn_tc_grads(Ctx* c, const AttnArgs& p, bool want_dkdv, std::string& err) {
     ProfScope prof_(c, "attn.bwd_dq");
     const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);   // persistent: one CTA per SM at most
     const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
-    attn_tc_dq_kernel<<<grid, kThreadsTC, smem_req(Q_SMEM), c->stream>>>(mq, mdo, mk, mv, mo, mdq, a);
+    launch_pdl(c, attn_tc_dq_kernel, grid, kThreadsTC, smem_req(Q_SMEM), mq, mdo, mk, mv, mo, mdq, a);
     if (check_launch("attn tc dq", err)) return 1;
   }
   if (want_dkdv) {
@@ -1106,7 +1112,7 @@ int attn_tc_grads(Ctx* c, const AttnArgs& p, bool want_dkdv, std::string& err) {
       return 1;
     ProfScope prof_(c, "attn.bwd_dkdv");
     dim3 grid((unsigned)((p.Sk + 127) / 128), (unsigned)(p.B * p.H));
-    attn_tc_dkdv_kernel<<<grid, kThreadsTC, smem_req(KV_SMEM), c->stream>>>(mk, mv, mq, mdo, a);
+    launch_pdl(c, attn_tc_dkdv_kernel, grid, kThreadsTC, smem_req(KV_SMEM), mk, mv, mq, mdo, a);
     if (check_launch("attn tc dkdv", err)) return 1;
   }
   return 0;

@@ -18,6 +18,7 @@ namespace {
 __global__ void rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D, const float* __restrict__ gamma,
                                        const float* __restrict__ sc, const float* __restrict__ sh, long mod_stride,
                                        int tps, float eps, __nv_bfloat16* __restrict__ h, float* __restrict__ rstd) {
+  pdl_prologue();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= T) return;
   const int lane = threadIdx.x & 31;
@@ -56,6 +57,7 @@ __global__ void rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D
 __global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float* __restrict__ x,
                                        const float* __restrict__ rstd, int T, int D, const float* __restrict__ gamma,
                                        const float* __restrict__ sc, long mod_stride, int tps, float* __restrict__ gx) {
+  pdl_prologue();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= T) return;
   const int lane = threadIdx.x & 31;
@@ -120,6 +122,7 @@ __device__ __forceinline__ float4 rope_cs2(const float2* __restrict__ tab, int p
 __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
                                      int tps, float eps, int rot, const float2* __restrict__ tab,
                                      __nv_bfloat16* __restrict__ out) {
+  pdl_prologue();
   const int nslices = slices.n;
   const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (pair >= H * nslices) return;
@@ -164,6 +167,7 @@ __global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int nco
 
 __global__ void head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y, int T, int ncols, int H,
                                      HeadSlice sl, int tps, int rot, const float2* __restrict__ tab, float* dy) {
+  pdl_prologue();
   const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (h >= H) return;
   const int lane = threadIdx.x & 31;
@@ -215,6 +219,7 @@ __global__ void head_prep_bwd_kernel(const float* g, long g_ld, const float* __r
 __global__ void gate_residual_kernel(const float* __restrict__ x_in, const float* __restrict__ y,
                                      const float* __restrict__ gate, long gstride, int T, int D, int tps,
                                      float* __restrict__ x_out) {
+  pdl_prologue();
   const int cidx = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (cidx >= D) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
@@ -229,6 +234,7 @@ __global__ void gate_residual_kernel(const float* __restrict__ x_in, const float
 
 __global__ void gate_bwd_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride, int T,
                                 int D, int tps, float* __restrict__ dy) {
+  pdl_prologue();
   const int cidx = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (cidx >= D) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
@@ -240,6 +246,7 @@ __global__ void gate_bwd_kernel(const float* __restrict__ gx, const float* __res
 }
 
 __global__ void add_kernel(const float* __restrict__ x, const float* __restrict__ y, long n, float* __restrict__ out) {
+  pdl_prologue();
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) out[i] = x[i] + y[i];
 }
 
@@ -248,6 +255,7 @@ __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x))
 // SwiGLU over rows: f[t] = [val (I) | gate (I)], a[t] = val * silu(gate).  Grid (I / 4 / 256
 // column blocks, T rows): each thread owns 4 consecutive columns of one row (128-bit accesses).
 __global__ void swiglu_fwd_kernel(const float* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
+  pdl_prologue();
   const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
@@ -263,6 +271,7 @@ __global__ void swiglu_fwd_kernel(const float* __restrict__ f, int T, int I, __n
 
 __global__ void swiglu_bwd_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
                                   float* __restrict__ df) {
+  pdl_prologue();
   const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
@@ -285,6 +294,7 @@ __global__ void swiglu_bwd_kernel(const float* __restrict__ da, const float* __r
 }
 
 __global__ void silu_bf16_kernel(const float* __restrict__ x, long n, __nv_bfloat16* __restrict__ out) {
+  pdl_prologue();
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const float v = x[i];
     out[i] = __float2bfloat16_rn(v * sigm(v));
@@ -293,6 +303,7 @@ __global__ void silu_bf16_kernel(const float* __restrict__ x, long n, __nv_bfloa
 
 __global__ void modulation_kernel(const float* __restrict__ ssg, const float* __restrict__ gcond, int B, int D,
                                   float* __restrict__ mod) {
+  pdl_prologue();
   const long n = (long)B * 6 * D;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const long j = i % (6L * D);
@@ -305,6 +316,7 @@ __global__ void modulation_kernel(const float* __restrict__ ssg, const float* __
 
 __global__ void mse_kernel(const float* __restrict__ vel, const float* __restrict__ tgt, long per, float inv,
                            float* __restrict__ loss, float* __restrict__ dvel) {
+  pdl_prologue();
   const int b = blockIdx.y;
   float acc = 0.f;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (long)gridDim.x * blockDim.x) {
@@ -327,6 +339,7 @@ __global__ void mse_kernel(const float* __restrict__ vel, const float* __restric
 __global__ void copy_rows_kernel(const float* __restrict__ src, int src_rows_per, int src_off, float* __restrict__ dst,
                                  __nv_bfloat16* __restrict__ dst_bf, int dst_rows_per, int dst_off, int B, int rows,
                                  int D) {
+  pdl_prologue();
   const long n = (long)B * rows * D;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const long d = i % D, r = (i / D) % rows, b = i / ((long)D * rows);
@@ -349,14 +362,14 @@ int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, 
                       long mod_stride, int tps, float eps, __nv_bfloat16* h, float* rstd, std::string& err) {
   if (D % 4) { err = "rms_norm: D % 4"; return 1; }
   ProfScope prof_(c, "rmsnorm_mod_fwd");
-  rmsnorm_mod_fwd_kernel<<<(unsigned)((T + 7) / 8), 256, 0, c->stream>>>(x, T, D, gamma, sc, sh, mod_stride, tps, eps, h, rstd);
+  launch_pdl(c, rmsnorm_mod_fwd_kernel, (unsigned)((T + 7) / 8), 256, 0, x, T, D, gamma, sc, sh, mod_stride, tps, eps, h, rstd);
   return check_launch("rmsnorm_mod_fwd", err);
 }
 
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
                       const float* sc, long mod_stride, int tps, float* gx, std::string& err) {
   ProfScope prof_(c, "rmsnorm_mod_bwd");
-  rmsnorm_mod_bwd_kernel<<<(unsigned)((T + 7) / 8), 256, 0, c->stream>>>(dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx);
+  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)((T + 7) / 8), 256, 0, dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx);
   return check_launch("rmsnorm_mod_bwd", err);
 }
 
@@ -399,7 +412,7 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   ProfScope prof_(c, "head_prep_fwd");
   if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
-  head_prep_fwd_kernel<<<grid, 256, 0, c->stream>>>(y, T, ncols, H, hs, tps, eps, rot, tab, out);
+  launch_pdl(c, head_prep_fwd_kernel, grid, 256, 0, y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
 
@@ -410,7 +423,7 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
   ProfScope prof_(c, "head_prep_bwd");
   if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
-  head_prep_bwd_kernel<<<grid, 256, 0, c->stream>>>(g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
+  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
   return check_launch("head_prep_bwd", err);
 }
 
@@ -418,8 +431,7 @@ int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate
                     float* x_out, std::string& err) {
   ProfScope prof_(c, "gate_residual");
   if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
-  gate_residual_kernel<<<dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0,
-                         c->stream>>>(x_in, y, gate, gstride, T, D, tps, x_out);
+  launch_pdl(c, gate_residual_kernel, dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, x_in, y, gate, gstride, T, D, tps, x_out);
   return check_launch("gate_residual", err);
 }
 
@@ -427,39 +439,39 @@ int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gstride, int T, 
                std::string& err) {
   ProfScope prof_(c, "gate_bwd");
   if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
-  gate_bwd_kernel<<<dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(gx, gate, gstride, T, D, tps, dy);
+  launch_pdl(c, gate_bwd_kernel, dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, gx, gate, gstride, T, D, tps, dy);
   return check_launch("gate_bwd", err);
 }
 
 int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err) {
   ProfScope prof_(c, "add");
-  add_kernel<<<gs(n), 256, 0, c->stream>>>(x, y, n, out);
+  launch_pdl(c, add_kernel, gs(n), 256, 0, x, y, n, out);
   return check_launch("add", err);
 }
 
 int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err) {
   ProfScope prof_(c, "swiglu_fwd");
   if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
-  swiglu_fwd_kernel<<<dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(f, T, I, a);
+  launch_pdl(c, swiglu_fwd_kernel, dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, f, T, I, a);
   return check_launch("swiglu_fwd", err);
 }
 
 int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err) {
   ProfScope prof_(c, "swiglu_bwd");
   if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
-  swiglu_bwd_kernel<<<dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, c->stream>>>(da, f, T, I, df);
+  launch_pdl(c, swiglu_bwd_kernel, dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, da, f, T, I, df);
   return check_launch("swiglu_bwd", err);
 }
 
 int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err) {
   ProfScope prof_(c, "silu");
-  silu_bf16_kernel<<<gs(n), 256, 0, c->stream>>>(x, n, out);
+  launch_pdl(c, silu_bf16_kernel, gs(n), 256, 0, x, n, out);
   return check_launch("silu", err);
 }
 
 int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err) {
   ProfScope prof_(c, "modulation");
-  modulation_kernel<<<gs((long)B * 6 * D), 256, 0, c->stream>>>(ssg, gcond, B, D, mod);
+  launch_pdl(c, modulation_kernel, gs((long)B * 6 * D), 256, 0, ssg, gcond, B, D, mod);
   return check_launch("modulation", err);
 }
 
@@ -467,14 +479,14 @@ int k_mse(Ctx* c, const float* vel, const float* target, int B, long per, float*
   ProfScope prof_(c, "mse");
   if (cudaMemsetAsync(loss, 0, sizeof(float) * B, c->stream) != cudaSuccess) return check_launch("mse memset", err);
   dim3 grid(16, (unsigned)B);
-  mse_kernel<<<grid, 256, 0, c->stream>>>(vel, target, per, 1.0f / (float)per, loss, dvel);
+  launch_pdl(c, mse_kernel, grid, 256, 0, vel, target, per, 1.0f / (float)per, loss, dvel);
   return check_launch("mse", err);
 }
 
 int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __nv_bfloat16* dst_bf,
                 int dst_rows_per, int dst_off, int B, int rows, int D, std::string& err) {
   ProfScope prof_(c, "copy_rows");
-  copy_rows_kernel<<<gs((long)B * rows * D), 256, 0, c->stream>>>(src, src_rows_per, src_off, dst, dst_bf, dst_rows_per,
+  launch_pdl(c, copy_rows_kernel, gs((long)B * rows * D), 256, 0, src, src_rows_per, src_off, dst, dst_bf, dst_rows_per,
                                                                   dst_off, B, rows, D);
   return check_launch("copy_rows", err);
 }

@@ -79,6 +79,7 @@ __device__ __forceinline__ ItemPos locate(const R16Problem* probs, const int* it
 __global__ void __launch_bounds__(kThreads, 1)
     r16_group_kernel(const R16Problem* __restrict__ probs, int nprob, int nitems, int* err) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   int* item0 = reinterpret_cast<int*>(smem + kOffItem0);
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
 
   auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
     if (*abort_flag) return false;
@@ -325,7 +327,7 @@ int r16_group_run(Ctx* c, const R16Group& g, const char* name, std::string& err)
   }
   const int grid = std::min<long>(g.nitems, (long)c->sm_count);
   ProfScope prof_(c, name);
-  r16_group_kernel<<<grid, kThreads, kDyn, c->stream>>>(static_cast<const R16Problem*>(g.table), g.nprob, g.nitems,
+  launch_pdl(c, r16_group_kernel, grid, kThreads, kDyn, static_cast<const R16Problem*>(g.table), g.nprob, g.nitems,
                                                         c->d_err);
   return check_launch("r16_group", err);
 }

@@ -132,7 +132,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
   {
     ProfScope prof_(c, d.name);
-    kern<<<grid, R::THREADS, L::DYN, c->stream>>>(ta, tb, tbs, tea, teb, tout, a);
+    launch_pdl(c, kern, grid, R::THREADS, L::DYN, ta, tb, tbs, tea, teb, tout, a);
     if (check_launch("gemm_tc", err)) return 1;
   }
   return 0;
@@ -184,15 +184,17 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
   const long tiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + BN - 1) / BN);
   const long clusters = tiles < (long)max_clusters ? tiles : (long)max_clusters;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
+  cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
   at[0].val.clusterDim.x = 2; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = use_pdl(c) ? 1 : 0;
   cfg.gridDim = dim3((unsigned)(2 * clusters));
   cfg.blockDim = dim3(kPairThreads);
   cfg.dynamicSmemBytes = L::DYN;
   cfg.stream = c->stream;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   ProfScope prof_(c, d.name);
   if (cudaLaunchKernelEx(&cfg, kern, ta, tb, tea, teb, tout, a) != cudaSuccess) return check_launch("gemm_tc2", err);
   return check_launch("gemm_tc2", err);

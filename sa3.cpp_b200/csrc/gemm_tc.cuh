@@ -328,6 +328,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
   static_assert(!T::mn || BN % 64 == 0, "MN-major B tiles are built from 64-wide atoms");
 
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -377,6 +378,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
 
   auto wait = [&](uint64_t* bar, uint32_t parity, int code) -> bool {
     if (*abort_flag) return false;

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   static_assert(!BMN || L::BH % 64 == 0, "MN-major B halves are built from 64-wide atoms");
 
   extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();   // the next kernel may be scheduled once every CTA of this grid runs
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   cluster_sync_all();      // barriers of both CTAs initialised, TMEM allocated in both
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  pdl_wait();      // outputs of earlier kernels are read only from here on
 
   auto wait = [&](uint64_t* bar, uint32_t parity, int code, bool cluster_scope) -> bool {
     if (*abort_flag) return false;

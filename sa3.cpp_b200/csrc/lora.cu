@@ -16,6 +16,7 @@ namespace sa3k {
 constexpr int R = 16;   // padded rank
 
 __global__ void cvt_bf16_kernel(const float* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
+  pdl_prologue();
   const int64_t n4 = n / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
@@ -38,6 +39,7 @@ __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __
                                     int64_t in, int64_t out, __nv_bfloat16* __restrict__ a_bf,
                                     __nv_bfloat16* __restrict__ at_x, __nv_bfloat16* __restrict__ b_x,
                                     __nv_bfloat16* __restrict__ bt_bf) {
+  pdl_prologue();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   for (int64_t k = t0; k < in * 64; k += stride) {
@@ -59,6 +61,7 @@ __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __
 // AAt[r1][r2] = sum_i A[r1][i] A[r2][i] (f32 accumulate).  Block r1 of 16; each of its 256
 // threads sums a strided slice of `in` for all 16 r2, then the block reduces.
 __global__ void aat_kernel(const float* __restrict__ A, int rank, int64_t in, float* __restrict__ aat) {
+  pdl_prologue();
   const int r1 = blockIdx.x;
   float acc[R];
 #pragma unroll
@@ -93,6 +96,7 @@ __global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __re
                                  int64_t out, const float* __restrict__ aat, const float* __restrict__ bns,
                                  const float* __restrict__ m, float s, float* __restrict__ nsq,
                                  float* __restrict__ g) {
+  pdl_prologue();
   __shared__ float saat[R * R];
   saat[threadIdx.x % (R * R)] = aat[threadIdx.x % (R * R)];
   __syncthreads();
@@ -135,6 +139,7 @@ __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __
                                    int T, int D, int tps, const float* __restrict__ y, const float* __restrict__ bias,
                                    const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
                                    float* __restrict__ dg) {
+  pdl_prologue();
   const int c0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (c0 >= D) return;
   const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
@@ -186,6 +191,7 @@ __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __
 __global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
                                      const float* __restrict__ bias, const float* __restrict__ g,
                                      __nv_bfloat16* __restrict__ dz, float* __restrict__ dg) {
+  pdl_prologue();
   const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
@@ -251,6 +257,7 @@ __global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const float* 
 // The same three preparations for every adapter of a model in one launch each (grid.y = adapter),
 // driven by a device array of PrepDesc built once when the adapters are bound.
 __global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
+  pdl_prologue();
   const PrepDesc d = descs[blockIdx.y];
   const int stride = gridDim.x * blockDim.x;
   const int t0 = blockIdx.x * blockDim.x + threadIdx.x;
@@ -270,6 +277,7 @@ __global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
 }
 
 __global__ void aat_all_kernel(const PrepDesc* __restrict__ descs) {
+  pdl_prologue();
   const PrepDesc d = descs[blockIdx.y];
   if (!d.dora) return;
   const int r1 = blockIdx.x;
@@ -299,6 +307,7 @@ __global__ void aat_all_kernel(const PrepDesc* __restrict__ descs) {
 }
 
 __global__ void dora_norm_all_kernel(const PrepDesc* __restrict__ descs) {
+  pdl_prologue();
   const PrepDesc d = descs[blockIdx.y];
   if (!d.dora) return;
   __shared__ float saat[R * R];
@@ -331,6 +340,7 @@ __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* _
                                     const float* __restrict__ bias, const float* __restrict__ g,
                                     int64_t S, int64_t out, __nv_bfloat16* __restrict__ dz,
                                     float* __restrict__ dg) {
+  pdl_prologue();
   const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= out) return;
   const int64_t t0 = (int64_t)blockIdx.y * kProTok;
@@ -419,12 +429,14 @@ __global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
     const float* __restrict__ nsq, const float* __restrict__ g, const float* __restrict__ dg, float s,
     float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __nv_bfloat16* __restrict__ cb,
     float* __restrict__ c3) {
+  pdl_prologue();
   dora_bwd_rows(blockIdx.x, pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_accumulate, dB, cb, c3);
 }
 
 // All DoRA adapters of a group at once: blockIdx.y = adapter, blockIdx.x = 128-row block of its
 // output rows (blocks past an adapter's rows return at once).  dm, dB accumulate.
 __global__ void __launch_bounds__(kDoraRows) dora_bwd_all_kernel(const PrepDesc* __restrict__ descs) {
+  pdl_prologue();
   const PrepDesc& d = descs[blockIdx.y];
   if (!d.dora || (int64_t)blockIdx.x * kDoraRows >= d.out) return;
   dora_bwd_rows(blockIdx.x, d.pt, d.B, d.rank, d.out, d.aat, d.nsq, d.g, d.dg, d.s, d.dm, 1, d.dB, d.cb, d.c3);
@@ -433,6 +445,7 @@ __global__ void __launch_bounds__(kDoraRows) dora_bwd_all_kernel(const PrepDesc*
 // dA[r][i] += 2 sum_q c3[r][q] A[q][i] for all DoRA adapters: blockIdx.y = adapter, 256 (r, i)
 // entries per block.
 __global__ void dora_da_c3_all_kernel(const PrepDesc* __restrict__ descs) {
+  pdl_prologue();
   const PrepDesc& d = descs[blockIdx.y];
   if (!d.dora) return;
   __shared__ float s3[R * R];
@@ -451,6 +464,7 @@ __global__ void dora_da_c3_all_kernel(const PrepDesc* __restrict__ descs) {
 // dA[r][i] += 2 sum_k c3[r][k] A[k][i]
 __global__ void dora_da_c3_kernel(const float* __restrict__ c3, const float* __restrict__ A, int rank,
                                   int64_t in, float* __restrict__ dA) {
+  pdl_prologue();
   __shared__ float s3[R * R];
   if (threadIdx.x < R * R) s3[threadIdx.x] = c3[threadIdx.x];
   __syncthreads();
@@ -472,7 +486,7 @@ static unsigned grid1d(int64_t n, int threads, int cap = 148 * 16) {
 
 int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err) {
   ProfScope prof_(c, "cvt_bf16");
-  cvt_bf16_kernel<<<grid1d(n / 4 + 1, 256), 256, 0, c->stream>>>(src, n, dst);
+  launch_pdl(c, cvt_bf16_kernel, grid1d(n / 4 + 1, 256), 256, 0, src, n, dst);
   return check_launch("cvt_bf16", err);
 }
 
@@ -480,21 +494,21 @@ int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, float s, in
                    __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
                    std::string& err) {
   ProfScope prof_(c, "prep_adapter");
-  prep_adapter_kernel<<<grid1d((in + out) * 64, 256), 256, 0, c->stream>>>(A, B, rank, s, in, out, a_bf, at_x, b_x,
+  launch_pdl(c, prep_adapter_kernel, grid1d((in + out) * 64, 256), 256, 0, A, B, rank, s, in, out, a_bf, at_x, b_x,
                                                                              bt_bf);
   return check_launch("prep_adapter", err);
 }
 
 int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err) {
   ProfScope prof_(c, "aat");
-  aat_kernel<<<R, 256, 0, c->stream>>>(A, rank, in, aat);
+  launch_pdl(c, aat_kernel, R, 256, 0, A, rank, in, aat);
   return check_launch("aat", err);
 }
 
 int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                 const float* bns, const float* m, float s, float* nsq, float* g, std::string& err) {
   ProfScope prof_(c, "dora_norm");
-  dora_norm_kernel<<<(unsigned)((out + 255) / 256), 256, 0, c->stream>>>(pt, B, rank, out, aat, bns, m, s, nsq, g);
+  launch_pdl(c, dora_norm_kernel, (unsigned)((out + 255) / 256), 256, 0, pt, B, rank, out, aat, bns, m, s, nsq, g);
   return check_launch("dora_norm", err);
 }
 
@@ -502,7 +516,7 @@ int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, c
                    int64_t out, __nv_bfloat16* dz, float* dg, std::string& err) {
   ProfScope prof_(c, "bwd_prologue");
   dim3 grid((unsigned)((out + 255) / 256), (unsigned)((S + kProTok - 1) / kProTok));
-  bwd_prologue_kernel<<<grid, 256, 0, c->stream>>>(dy, y, bias, g, S, out, dz, dg);
+  launch_pdl(c, bwd_prologue_kernel, grid, 256, 0, dy, y, bias, g, S, out, dz, dg);
   return check_launch("bwd_prologue", err);
 }
 
@@ -510,7 +524,7 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
                float* dB, __nv_bfloat16* cb, float* c3, std::string& err) {
   ProfScope prof_(c, "dora_bwd");
-  dora_bwd_kernel<<<(unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, c->stream>>>(
+  launch_pdl(c, dora_bwd_kernel, (unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, 
       pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_acc, dB, cb, c3);
   return check_launch("dora_bwd", err);
 }
@@ -521,8 +535,7 @@ int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int 
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "gate: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "gate_bwd_dz");
-  gate_bwd_dz_kernel<<<dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0,
-                       c->stream>>>(gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
+  launch_pdl(c, gate_bwd_dz_kernel, dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0, gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
   return check_launch("gate_bwd_dz", err);
 }
 
@@ -532,45 +545,43 @@ int k_swiglu_bwd_dz(Ctx* c, const float* da, const float* f, int T, int I, const
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 2 * I, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "swiglu_bwd_dz");
-  swiglu_bwd_dz_kernel<<<dim3((unsigned)((I / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0,
-                         c->stream>>>(da, f, T, I, bias, g, dz, dg);
+  launch_pdl(c, swiglu_bwd_dz_kernel, dim3((unsigned)((I / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0, da, f, T, I, bias, g, dz, dg);
   return check_launch("swiglu_bwd_dz", err);
 }
 
 int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
   ProfScope prof_(c, "prep_adapter");
-  prep_all_kernel<<<dim3(48, (unsigned)n), 256, 0, c->stream>>>(descs);
+  launch_pdl(c, prep_all_kernel, dim3(48, (unsigned)n), 256, 0, descs);
   return check_launch("prep_all", err);
 }
 
 int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
   ProfScope prof_(c, "aat");
-  aat_all_kernel<<<dim3(R, (unsigned)n), 256, 0, c->stream>>>(descs);
+  launch_pdl(c, aat_all_kernel, dim3(R, (unsigned)n), 256, 0, descs);
   return check_launch("aat_all", err);
 }
 
 int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err) {
   ProfScope prof_(c, "dora_norm");
-  dora_norm_all_kernel<<<dim3((unsigned)((max_out + 255) / 256), (unsigned)n), 256, 0, c->stream>>>(descs);
+  launch_pdl(c, dora_norm_all_kernel, dim3((unsigned)((max_out + 255) / 256), (unsigned)n), 256, 0, descs);
   return check_launch("dora_norm_all", err);
 }
 
 int k_dora_bwd_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err) {
   ProfScope prof_(c, "dora_bwd");
-  dora_bwd_all_kernel<<<dim3((unsigned)((max_out + kDoraRows - 1) / kDoraRows), (unsigned)n), kDoraRows, 0,
-                        c->stream>>>(descs);
+  launch_pdl(c, dora_bwd_all_kernel, dim3((unsigned)((max_out + kDoraRows - 1) / kDoraRows), (unsigned)n), kDoraRows, 0, descs);
   return check_launch("dora_bwd_all", err);
 }
 
 int k_dora_da_c3_all(Ctx* c, const PrepDesc* descs, int n, std::string& err) {
   ProfScope prof_(c, "dora_da_c3");
-  dora_da_c3_all_kernel<<<dim3(64, (unsigned)n), 256, 0, c->stream>>>(descs);
+  launch_pdl(c, dora_da_c3_all_kernel, dim3(64, (unsigned)n), 256, 0, descs);
   return check_launch("dora_da_c3_all", err);
 }
 
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err) {
   ProfScope prof_(c, "dora_da_c3");
-  dora_da_c3_kernel<<<(unsigned)(((int64_t)rank * in + 255) / 256), 256, 0, c->stream>>>(c3, A, rank, in, dA);
+  launch_pdl(c, dora_da_c3_kernel, (unsigned)(((int64_t)rank * in + 255) / 256), 256, 0, c3, A, rank, in, dA);
   return check_launch("dora_da_c3", err);
 }
 

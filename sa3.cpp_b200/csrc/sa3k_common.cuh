@@ -40,6 +40,19 @@ __device__ __forceinline__ void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ------------------------------------------------------------------------------ PDL
+// Programmatic dependent launch: every kernel of the library is launched with programmatic
+// stream serialization allowed (launch_pdl).  pdl_trigger lets the next kernel of the stream be
+// scheduled once every CTA of this grid has started; pdl_wait blocks until the previous grid has
+// completed and its memory is visible, so nothing that a predecessor writes may be read before
+// it.  Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_prologue() {
+  pdl_trigger();
+  pdl_wait();
+}
+
 // ------------------------------------------------------------------------------ mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace sa3k {
@@ -59,6 +60,7 @@ struct Ctx {
   int tile_n = 0;                    // main-GEMM N tile: 0 = cost model, 128 or 256 = fixed
   int gemm_pair = 1;                 // CTA-pair (cta_group::2) GEMMs: 0 never, 1 where they pay, 2 always
   bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
+  bool pdl = true;                   // programmatic dependent launch between consecutive kernels
   // NeoX RoPE (cos, sin) table for (positions, rot, base), kept in scratch slot kSlotRope
   const void* rope_tab = nullptr;
   int rope_tps = 0, rope_rot = 0;
@@ -83,6 +85,32 @@ typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 PFN_encodeTiled encode_tiled_fn(std::string& err);
+
+// Programmatic dependent launch for eager launches (measured on the DiT step: it hides part of
+// each launch's latency when kernels are launched one by one, while a captured CUDA graph replays
+// faster without the programmatic edges).
+inline bool use_pdl(Ctx* c) {
+  if (!c->pdl) return false;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  return cudaStreamIsCapturing(c->stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+}
+
+// Launch `kern` on the context's stream with programmatic stream serialization (the kernel
+// starts with pdl_prologue or waits with pdl_wait before reading its predecessors' outputs).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(Ctx* c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = c->stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = use_pdl(c) ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 inline int check_launch(const char* what, std::string& err) {
   const cudaError_t e = cudaGetLastError();
