@@ -633,7 +633,7 @@ int sa3k_head_prep_bwd(sa3k_ctx* ctx, const float* g, int64_t g_ld, const float*
   HeadSlice hs;
   hs.col = slice->col; hs.gamma = slice->gamma; hs.rope = slice->rope; hs.rstd = slice->rstd;
   std::string e;
-  if (k_head_prep_bwd(&ctx->c, g, (long)g_ld, y, T, ncols, H, hs, tps, rot, rope_base, dy, e))
+  if (k_head_prep_bwd(&ctx->c, g, (long)g_ld, y, T, ncols, H, hs, tps, rot, rope_base, dy, nullptr, e))
     return fill_err(err, err_len, e);
   return 0;
 }

@@ -37,9 +37,11 @@ int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err);
 int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, const float* sc, const float* sh,
                       long mod_stride, int tokens_per_sample, float eps, __nv_bfloat16* h, float* rstd,
                       std::string& err);
-// gx += d/dx of the above for upstream dh (gamma, sc, sh are frozen)
+// gx += d/dx of the above for upstream dh (gamma, sc, sh are frozen); gx_bf (nullable) also
+// receives the updated gx as bf16
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
-                      const float* sc, long mod_stride, int tokens_per_sample, float* gx, std::string& err);
+                      const float* sc, long mod_stride, int tokens_per_sample, float* gx, __nv_bfloat16* gx_bf,
+                      std::string& err);
 
 // Per-head q/k preparation of a fused projection output y[T][ncols] (f32): for each slice (a
 // column offset that is a multiple of the head width 64): rms-norm with gamma (if gamma), then
@@ -53,9 +55,17 @@ struct HeadSlice {
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
                     int tokens_per_sample, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err);
 // Backward of one slice: g[T][H*64] (f32, gradient w.r.t. the prepared slice) -> dy slice of
-// dy[T][ncols] (f32, overwritten), using the forward input y and the saved rstd.
+// dy[T][ncols] (f32, overwritten; or, with dy_bf, written as bf16 there instead), using the
+// forward input y and the saved rstd.
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& s,
-                    int tokens_per_sample, int rot, float rope_base, float* dy, std::string& err);
+                    int tokens_per_sample, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf,
+                    std::string& err);
+// Self-attention q/k/v head preparation backward (dq3 = [dq | dk | dv] f32, qkv = the projection
+// output) fused with the qkv projection's backward prologue: dz = bf16(g * dy) [T][3D] and
+// dg[3D] = colsum(dy * qkv / g) (DoRA g; null: plain bf16 conversion, dg untouched).
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, const float* rq, const float* rk,
+                 const float* gq, const float* gk, int tokens_per_sample, int rot, float rope_base, const float* g,
+                 __nv_bfloat16* dz, float* dg, std::string& err);
 
 // x_out = x_in + y * gate[sample]  (gate already sigmoid(1 - g)); x_out may alias x_in
 int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate, long gate_stride, int T, int D,

@@ -509,9 +509,10 @@ static int dit_step(DitModel& m, std::string& err) {
                         dg_of(m, tp), err))
       return 1;
     if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
-    if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, err)) return 1;
+    // (the norm backward also leaves gx as bf16 in m.dz: the input of the cross.out backward)
+    if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, m.dz, err)) return 1;
     // cross-attention branch (context and its projections are frozen: only dq flows)
-    if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, m.gx, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
+    if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, nullptr, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
     {
       AttnArgs ca;
       ca.B = B; ca.H = H; ca.Sq = S; ca.Sk = C; ca.scale = scale; ca.window = -1;
@@ -526,10 +527,11 @@ static int dit_step(DitModel& m, std::string& err) {
       if (attn_backward(c, ca, false, err)) return 1;
       HeadSlice hs;
       hs.col = 0; hs.gamma = g_cq; hs.rstd = a.rcq;
-      if (k_head_prep_bwd(c, m.dtmp, D, a.qf, (int)M, D, H, hs, S, k.rot, k.rope_base, m.dh, err)) return 1;
+      // bf16 gradient straight into m.dz: the input of the cross.q backward
+      if (k_head_prep_bwd(c, m.dtmp, D, a.qf, (int)M, D, H, hs, S, k.rot, k.rope_base, nullptr, m.dz, err)) return 1;
     }
-    if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, m.dh, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
-    if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, err)) return 1;
+    if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, nullptr, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
+    if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, nullptr, err)) return 1;
     // self-attention branch
     if (k_gate_bwd_dz(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, a.yo, nullptr,
                       to && to->prep.dora() ? to->prep.g : nullptr, dz_of(m, to), dg_of(m, to), err))
@@ -549,14 +551,13 @@ static int dit_step(DitModel& m, std::string& err) {
       sa.dk = m.dq3 + D; sa.dk_sb = sa.dq_sb; sa.dk_sh = 64; sa.dk_ld = Q;
       sa.dv = m.dq3 + 2 * D; sa.dv_sb = sa.dq_sb; sa.dv_sh = 64; sa.dv_ld = Q;
       if (attn_backward(c, sa, true, err)) return 1;
-      HeadSlice hq, hk;
-      hq.col = 0; hq.gamma = g_q; hq.rope = 1; hq.rstd = a.rq;
-      hk.col = D; hk.gamma = g_k; hk.rope = 1; hk.rstd = a.rk;
-      if (k_head_prep_bwd(c, m.dq3, Q, a.qkv, (int)M, Q, H, hq, S, k.rot, k.rope_base, m.dq3, err)) return 1;
-      if (k_head_prep_bwd(c, m.dq3 + D, Q, a.qkv, (int)M, Q, H, hk, S, k.rot, k.rope_base, m.dq3, err)) return 1;
+      // q / k head preparation backward fused with the qkv projection's prologue
+      if (k_qkv_bwd_dz(c, m.dq3, a.qkv, (int)M, D, H, a.rq, a.rk, g_q, g_k, S, k.rot, k.rope_base,
+                       tq && tq->prep.dora() ? tq->prep.g : nullptr, dz_of(m, tq), dg_of(m, tq), err))
+        return 1;
     }
-    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, m.dq3, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
-    if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, err)) return 1;
+    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, nullptr, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
+    if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, nullptr, err)) return 1;
   }
   // ---------------- adapter gradients, grouped over every adapter of the step: the DoRA row terms
   // (dm, dB, and the cb / c3 factors of dA), then one launch for all dB += s dz^T u,

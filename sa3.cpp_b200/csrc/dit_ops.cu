@@ -56,7 +56,8 @@ __global__ void rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D
 
 __global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float* __restrict__ x,
                                        const float* __restrict__ rstd, int T, int D, const float* __restrict__ gamma,
-                                       const float* __restrict__ sc, long mod_stride, int tps, float* __restrict__ gx) {
+                                       const float* __restrict__ sc, long mod_stride, int tps, float* __restrict__ gx,
+                                       __nv_bfloat16* __restrict__ gx_bf) {
   pdl_prologue();
   const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   if (row >= T) return;
@@ -86,6 +87,12 @@ __global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float
     gv.z += r * (d.z * gm.z * (1.f + a.z) - v.z * r * dot);
     gv.w += r * (d.w * gm.w * (1.f + a.w) - v.w * r * dot);
     gr[i] = gv;
+    if (gx_bf) {
+      uint2 pk;
+      pk.x = pack_bf16x2(gv.x, gv.y);
+      pk.y = pack_bf16x2(gv.z, gv.w);
+      reinterpret_cast<uint2*>(gx_bf + (long)row * D)[i] = pk;
+    }
   }
 }
 
@@ -102,116 +109,233 @@ __global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __r
   tab[e] = make_float2(cs, sn);
 }
 
-// One warp per (slice, head) and kHeadRows consecutive token rows; lane l holds head elements
-// 2l and 2l + 1 (one 8-byte load and one 4-byte bf16x2 store per row).  All rows' loads are
-// issued before any row is processed.  RoPE partners: rot 32 pairs (i, i + 16), i < 16, live in
-// lanes l and l ^ 8 (lanes 0..15); rot 64 pairs (i, i + 32) in lanes l and l ^ 16.
+// Head preparation kernels: 8 lanes per head row.  Lane l of a warp: row group q = l >> 3 (four
+// token rows at a time), element chunk j = l & 7 (head elements 8j .. 8j + 7, two 16-byte loads).
+// Per-row sums take three shuffles inside the 8-lane group.  NeoX RoPE pairs (i, i + rot/2),
+// i < rot/2: rot 32 pairs chunks j and j ^ 2 (j < 4), rot 64 pairs chunks j and j ^ 4.  A block
+// is 8 warps on 8 consecutive heads of one slice (512 contiguous columns) and kHpRows token rows.
 struct HeadSlices {
   HeadSlice s[5];
   int n;
 };
-constexpr int kHeadRows = 8;
+constexpr int kHpRows = 32;
 
-// cos / sin of the two NeoX pairs (e & (rot/2 - 1)) of head elements e = 2l, 2l + 1
-__device__ __forceinline__ float4 rope_cs2(const float2* __restrict__ tab, int pos, int lane, int rot) {
-  const int half = rot / 2;
-  return *reinterpret_cast<const float4*>(tab + pos * half + ((2 * lane) & (half - 1)));
+__device__ __forceinline__ float sum8(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  v += __shfl_xor_sync(0xffffffffu, v, 2);
+  v += __shfl_xor_sync(0xffffffffu, v, 4);
+  return v;
 }
 
-// Grid (ceil(H * nslices / 8), ceil(T / kHeadRows)); warp w of block x = (slice, head) pair 8 x + w.
-__global__ void head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H, const HeadSlices slices,
-                                     int tps, float eps, int rot, const float2* __restrict__ tab,
-                                     __nv_bfloat16* __restrict__ out) {
+__device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
+  reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ void st8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+  uint4 o;
+  o.x = pack_bf16x2(v[0], v[1]);
+  o.y = pack_bf16x2(v[2], v[3]);
+  o.z = pack_bf16x2(v[4], v[5]);
+  o.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = o;
+}
+
+// RoPE of this lane's chunk j at position pos (inverse rotation when inv): first element of a pair
+// x cos -/+ partner sin, second partner sin +/- ... ; all lanes take part in the shuffles.
+__device__ __forceinline__ void rope8(float (&v)[8], int j, int pos, int rot, const float2* __restrict__ tab, bool inv) {
+  const int half = rot / 2, px = rot == 32 ? 2 : 4;
+  float pv[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) pv[k] = __shfl_xor_sync(0xffffffffu, v[k], px);
+  if (rot == 64 || j < 4) {
+    const bool first = (j & px) == 0;
+    const float4* cs = reinterpret_cast<const float4*>(tab + pos * half + ((8 * j) & (half - 1)));
+#pragma unroll
+    for (int k2 = 0; k2 < 4; ++k2) {
+      const float4 c = cs[k2];   // (cos, sin) of elements 2 k2 and 2 k2 + 1 of the chunk
+      const float c0 = c.x, s0 = inv ? -c.y : c.y, c1 = c.z, s1 = inv ? -c.w : c.w;
+      if (first) {
+        v[2 * k2] = v[2 * k2] * c0 - pv[2 * k2] * s0;
+        v[2 * k2 + 1] = v[2 * k2 + 1] * c1 - pv[2 * k2 + 1] * s1;
+      } else {
+        v[2 * k2] = pv[2 * k2] * s0 + v[2 * k2] * c0;
+        v[2 * k2 + 1] = pv[2 * k2 + 1] * s1 + v[2 * k2 + 1] * c1;
+      }
+    }
+  }
+}
+
+// Grid (ceil(H * nslices / 8), ceil(T / kHpRows)).
+__global__ void __launch_bounds__(256) head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H,
+                                                            const HeadSlices slices, int tps, float eps, int rot,
+                                                            const float2* __restrict__ tab,
+                                                            __nv_bfloat16* __restrict__ out) {
   pdl_prologue();
-  const int nslices = slices.n;
-  const int pair = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (pair >= H * nslices) return;
-  const int lane = threadIdx.x & 31;
-  const int si = pair % nslices, h = pair / nslices;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
+  const int pair = blockIdx.x * 8 + warp;
+  if (pair >= H * slices.n) return;
+  const int si = pair / H, h = pair % H;
   const HeadSlice sl = slices.s[si];
-  const int t0 = blockIdx.y * kHeadRows;
-  const float2 gm = sl.gamma ? reinterpret_cast<const float2*>(sl.gamma)[lane] : make_float2(1.f, 1.f);
-  float2 v[kHeadRows];
+  const int col = sl.col + h * 64 + 8 * j;
+  float gm[8];
+  if (sl.gamma) ld8(sl.gamma + 8 * j, gm);
+  else {
 #pragma unroll
-  for (int r = 0; r < kHeadRows; ++r)
-    v[r] = t0 + r < T ? reinterpret_cast<const float2*>(y + (long)(t0 + r) * ncols + sl.col + h * 64)[lane]
-                      : make_float2(0.f, 0.f);
+    for (int k = 0; k < 8; ++k) gm[k] = 1.f;
+  }
+  const int tb0 = blockIdx.y * kHpRows;
+  int pos = (tb0 + q) % tps;
+#pragma unroll 2
+  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
+    const int t = tb0 + 4 * it + q;
+    const bool valid = t < T;
+    float v[8];
+    if (valid) ld8(y + (long)t * ncols + col, v);
+    else {
 #pragma unroll
-  for (int r = 0; r < kHeadRows; ++r) {
-    const int t = t0 + r;
-    if (t >= T) break;
-    float a = v[r].x, b = v[r].y;
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+    }
     if (sl.gamma) {
-      const float rr = rsqrtf(warp_sum(a * a + b * b) / 64.f + eps);
-      if (lane == 0 && sl.rstd) sl.rstd[(long)t * H + h] = rr;
-      a *= rr * gm.x;
-      b *= rr * gm.y;
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+      const float r = rsqrtf(sum8(ss) / 64.f + eps);
+      if (valid && j == 0 && sl.rstd) sl.rstd[(long)t * H + h] = r;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] *= r * gm[k];
     }
-    if (sl.rope && (rot == 32 || rot == 64)) {
-      const int px = rot == 32 ? 8 : 16;
-      const float pa = __shfl_xor_sync(0xffffffffu, a, px), pb = __shfl_xor_sync(0xffffffffu, b, px);
-      if (rot == 64 || lane < 16) {
-        const float4 cs = rope_cs2(tab, t % tps, lane, rot);
-        if ((lane & px) == 0) {   // first element of the pair: x cos - partner sin
-          a = a * cs.x - pa * cs.y;
-          b = b * cs.z - pb * cs.w;
-        } else {                  // second: partner sin + x cos
-          a = pa * cs.y + a * cs.x;
-          b = pb * cs.w + b * cs.z;
-        }
-      }
-    }
-    reinterpret_cast<__nv_bfloat162*>(out + (long)t * ncols + sl.col + h * 64)[lane] = __floats2bfloat162_rn(a, b);
+    if (sl.rope && (rot == 32 || rot == 64)) rope8(v, j, pos, rot, tab, false);
+    if (valid) st8_bf16(out + (long)t * ncols + col, v);
+    pos += 4;
+    while (pos >= tps) pos -= tps;
   }
 }
 
-__global__ void head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y, int T, int ncols, int H,
-                                     HeadSlice sl, int tps, int rot, const float2* __restrict__ tab, float* dy) {
+// Backward of one slice.  Grid (ceil(H / 8), ceil(T / kHpRows)).
+__global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y,
+                                                            int T, int ncols, int H, HeadSlice sl, int tps, int rot,
+                                                            const float2* __restrict__ tab, float* dy,
+                                                            __nv_bfloat16* dy_bf) {
   pdl_prologue();
-  const int h = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
+  const int h = blockIdx.x * 8 + warp;
   if (h >= H) return;
-  const int lane = threadIdx.x & 31;
-  const int t0 = blockIdx.y * kHeadRows;
-  const float2 gm = sl.gamma ? reinterpret_cast<const float2*>(sl.gamma)[lane] : make_float2(1.f, 1.f);
-  float2 gv[kHeadRows], yv[kHeadRows];
-  float rs[kHeadRows];
+  float gm[8];
+  if (sl.gamma) ld8(sl.gamma + 8 * j, gm);
+  const int tb0 = blockIdx.y * kHpRows;
+  int pos = (tb0 + q) % tps;
+#pragma unroll 2
+  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
+    const int t = tb0 + 4 * it + q;
+    const bool valid = t < T;
+    float gv[8], yv[8];
+    float r = 0.f;
+    if (valid) {
+      ld8(g + (long)t * g_ld + h * 64 + 8 * j, gv);
+      if (sl.gamma) {
+        ld8(y + (long)t * ncols + sl.col + h * 64 + 8 * j, yv);
+        r = sl.rstd[(long)t * H + h];
+      }
+    } else {
 #pragma unroll
-  for (int r = 0; r < kHeadRows; ++r) {
-    const int t = t0 + r;
-    const bool in = t < T;
-    gv[r] = in ? reinterpret_cast<const float2*>(g + (long)t * g_ld + h * 64)[lane] : make_float2(0.f, 0.f);
-    yv[r] = in && sl.gamma ? reinterpret_cast<const float2*>(y + (long)t * ncols + sl.col + h * 64)[lane]
-                           : make_float2(0.f, 0.f);
-    rs[r] = in && sl.gamma ? sl.rstd[(long)t * H + h] : 0.f;
+      for (int k = 0; k < 8; ++k) gv[k] = yv[k] = 0.f;
+    }
+    if (sl.rope && (rot == 32 || rot == 64)) rope8(gv, j, pos, rot, tab, true);
+    if (sl.gamma) {
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        yv[k] *= r;            // normalized input
+        gv[k] *= gm[k];        // gradient w.r.t. the normalized input
+        dot = fmaf(gv[k], yv[k], dot);
+      }
+      const float mean = sum8(dot) / 64.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] = r * (gv[k] - yv[k] * mean);
+    }
+    if (valid) {
+      if (dy_bf) st8_bf16(dy_bf + (long)t * ncols + sl.col + h * 64 + 8 * j, gv);
+      else st8(dy + (long)t * ncols + sl.col + h * 64 + 8 * j, gv);
+    }
+    pos += 4;
+    while (pos >= tps) pos -= tps;
   }
+}
+
+// The self-attention head preparation's backward (q and k: inverse RoPE, then the per-head
+// rms-norm backward; v: identity) fused with the qkv projection's backward prologue: writes
+// dz = bf16(g * dy) and adds colsum(dy * y / g) into dg (DoRA; g null: dz = bf16(dy)), with
+// y = the projection output qkv (no bias).  Block = 8 warps on 8 consecutive head slices of
+// [q heads | k heads | v heads] and kHpRows token rows; each lane adds its 8 columns' dg sums
+// (summed over the warp's four row groups first) once.  Grid (ceil(3H / 8), ceil(T / kHpRows)).
+__global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
+                                                            const float* __restrict__ qkv, int T, int D, int H,
+                                                            const float* __restrict__ rq, const float* __restrict__ rk,
+                                                            const float* __restrict__ gq, const float* __restrict__ gk,
+                                                            int tps, int rot, const float2* __restrict__ tab,
+                                                            const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
+                                                            float* __restrict__ dg) {
+  pdl_prologue();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
+  const int hs = blockIdx.x * 8 + warp;
+  if (hs >= 3 * H) return;
+  const int slice = hs / H, h = hs % H;
+  const int ncols = 3 * D, col = slice * D + h * 64 + 8 * j;
+  const bool norm = slice < 2;
+  const float* rs = slice == 0 ? rq : rk;
+  float gm[8], gd[8], acc[8];
+  if (norm) ld8((slice == 0 ? gq : gk) + 8 * j, gm);
+  if (g) ld8(g + col, gd);
 #pragma unroll
-  for (int r = 0; r < kHeadRows; ++r) {
-    const int t = t0 + r;
-    if (t >= T) break;
-    float ga = gv[r].x, gb = gv[r].y;
-    if (sl.rope && (rot == 32 || rot == 64)) {   // inverse rotation of the gradient
-      const int px = rot == 32 ? 8 : 16;
-      const float pa = __shfl_xor_sync(0xffffffffu, ga, px), pb = __shfl_xor_sync(0xffffffffu, gb, px);
-      if (rot == 64 || lane < 16) {
-        const float4 cs = rope_cs2(tab, t % tps, lane, rot);
-        if ((lane & px) == 0) {
-          ga = ga * cs.x + pa * cs.y;
-          gb = gb * cs.z + pb * cs.w;
-        } else {
-          ga = -pa * cs.y + ga * cs.x;
-          gb = -pb * cs.w + gb * cs.z;
-        }
+  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+  const int tb0 = blockIdx.y * kHpRows;
+  int pos = (tb0 + q) % tps;
+  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
+    const int t = tb0 + 4 * it + q;
+    const bool valid = t < T;
+    float gv[8], yv[8];
+    float r = 0.f;
+    if (valid) {
+      ld8(dq3 + (long)t * ncols + col, gv);
+      if (norm || g) ld8(qkv + (long)t * ncols + col, yv);
+      if (norm) r = rs[(long)t * H + h];
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] = yv[k] = 0.f;
+    }
+    if (norm) {
+      if (rot == 32 || rot == 64) rope8(gv, j, pos, rot, tab, true);
+      float dot = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) dot = fmaf(gv[k] * gm[k], yv[k] * r, dot);
+      const float mean = sum8(dot) / 64.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] = r * (gv[k] * gm[k] - yv[k] * r * mean);
+    }
+    if (g) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        acc[k] = fmaf(gv[k], yv[k] / gd[k], acc[k]);
+        gv[k] *= gd[k];
       }
     }
-    if (sl.gamma) {
-      const float rr = rs[r];
-      const float na = yv[r].x * rr, nb = yv[r].y * rr;
-      const float da = ga * gm.x, db = gb * gm.y;
-      const float mean = warp_sum(da * na + db * nb) / 64.f;
-      ga = rr * (da - na * mean);
-      gb = rr * (db - nb * mean);
+    if (valid) st8_bf16(dz + (long)t * ncols + col, gv);
+    pos += 4;
+    while (pos >= tps) pos -= tps;
+  }
+  if (g) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], 8);
+      acc[k] += __shfl_xor_sync(0xffffffffu, acc[k], 16);
+      if (q == 0) atomicAdd(dg + col + k, acc[k]);
     }
-    reinterpret_cast<float2*>(dy + (long)t * ncols + sl.col + h * 64)[lane] = make_float2(ga, gb);
   }
 }
 
@@ -367,9 +491,10 @@ int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, 
 }
 
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
-                      const float* sc, long mod_stride, int tps, float* gx, std::string& err) {
+                      const float* sc, long mod_stride, int tps, float* gx, __nv_bfloat16* gx_bf, std::string& err) {
   ProfScope prof_(c, "rmsnorm_mod_bwd");
-  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)((T + 7) / 8), 256, 0, dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx);
+  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)((T + 7) / 8), 256, 0, dh, x, rstd, T, D, gamma, sc, mod_stride,
+             tps, gx, gx_bf);
   return check_launch("rmsnorm_mod_bwd", err);
 }
 
@@ -410,20 +535,33 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   const float2* tab = nullptr;
   if (any_rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
-  if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
-  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
+  if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
+  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
   launch_pdl(c, head_prep_fwd_kernel, grid, 256, 0, y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
 
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, const float* rq, const float* rk,
+                 const float* gq, const float* gk, int tps, int rot, float rope_base, const float* g, __nv_bfloat16* dz,
+                 float* dg, std::string& err) {
+  const float2* tab = nullptr;
+  if (rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
+  if ((T + kHpRows - 1) / kHpRows > 65535) { err = "qkv backward: too many rows"; return 1; }
+  if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 3 * D, c->stream) != cudaSuccess) return check_launch("memset", err);
+  ProfScope prof_(c, "qkv_bwd_dz");
+  launch_pdl(c, qkv_bwd_dz_kernel, dim3((unsigned)((3 * H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows)), 256, 0,
+             dq3, qkv, T, D, H, rq, rk, gq, gk, tps, rot, tab, g, dz, dg);
+  return check_launch("qkv_bwd_dz", err);
+}
+
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
-                    int tps, int rot, float rope_base, float* dy, std::string& err) {
+                    int tps, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf, std::string& err) {
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
-  if ((T + kHeadRows - 1) / kHeadRows > 65535) { err = "head prep: too many rows"; return 1; }
-  const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHeadRows - 1) / kHeadRows));
-  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy);
+  if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
+  const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
+  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy, dy_bf);
   return check_launch("head_prep_bwd", err);
 }
 
