@@ -133,19 +133,23 @@ __device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4
   *reinterpret_cast<uint2*>(dz) = pk;
 }
 
-// dy = gx * gate[sample] (the gate backward of src/dit.h:186-193).  Rows are processed four at a
-// time with all their loads issued first.
-__global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate, long gstride,
-                                   int T, int D, int tps, const float* __restrict__ y, const float* __restrict__ bias,
-                                   const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
-                                   float* __restrict__ dg) {
+// dy = gx * gate[sample] (the gate backward of src/dit.h:186-193).  Block (128, 4): thread x owns
+// 4 columns, thread y a quarter of the block's kFuseTok rows (four rows at a time, loads first);
+// dg is summed over y in shared memory before one atomic per column.
+__global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate,
+                                                          long gstride, int T, int D, int tps,
+                                                          const float* __restrict__ y, const float* __restrict__ bias,
+                                                          const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
+                                                          float* __restrict__ dg) {
   pdl_prologue();
+  __shared__ float4 red[4][128];
   const int c0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
-  if (c0 >= D) return;
-  const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
+  const bool col_ok = c0 < D;
+  const int rq = kFuseTok / 4;
+  const int t0 = blockIdx.y * kFuseTok + threadIdx.y * rq, t1 = min(T, t0 + rq);
   const bool dora = g != nullptr;
   float gv[4] = {1.f, 1.f, 1.f, 1.f}, inv[4] = {1.f, 1.f, 1.f, 1.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (dora) {
+  if (dora && col_ok) {
     const float4 g4 = *reinterpret_cast<const float4*>(g + c0);
     gv[0] = g4.x; gv[1] = g4.y; gv[2] = g4.z; gv[3] = g4.w;
 #pragma unroll
@@ -156,7 +160,7 @@ __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __
     }
   }
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int tb = t0; tb < t1; tb += 4) {
+  for (int tb = t0; tb < t1 && col_ok; tb += 4) {
     float4 gt[4], av[4], yv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -181,8 +185,20 @@ __global__ void gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __
     }
   }
   if (dora) {
+    red[threadIdx.y][threadIdx.x] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (threadIdx.y == 0 && col_ok) {
+      float4 sum = red[0][threadIdx.x];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) atomicAdd(dg + c0 + q, acc[q]);
+      for (int q = 1; q < 4; ++q) {
+        const float4 v = red[q][threadIdx.x];
+        sum.x += v.x; sum.y += v.y; sum.z += v.z; sum.w += v.w;
+      }
+      atomicAdd(dg + c0, sum.x);
+      atomicAdd(dg + c0 + 1, sum.y);
+      atomicAdd(dg + c0 + 2, sum.z);
+      atomicAdd(dg + c0 + 3, sum.w);
+    }
   }
 }
 
@@ -535,7 +551,8 @@ int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int 
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "gate: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "gate_bwd_dz");
-  launch_pdl(c, gate_bwd_dz_kernel, dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)), 128, 0, gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
+  launch_pdl(c, gate_bwd_dz_kernel, dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)),
+             dim3(128, 4), 0, gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
   return check_launch("gate_bwd_dz", err);
 }
 
