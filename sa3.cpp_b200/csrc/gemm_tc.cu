@@ -67,6 +67,40 @@ static int* split_counters(Ctx* c, std::string& err) {
   return p;
 }
 
+// Tail split: when the tiles leave a last, partial round on `slots` CTAs (or CTA pairs), split
+// each of those tiles' K range into parts spread over every slot; the parts add into the output,
+// which is zeroed first over the column band of the tail tiles unless the GEMM accumulates.
+// f32 output only (bf16 partial sums cannot be added), no split-K.
+static int plan_tail(Ctx* c, const GemmDesc& d, GemmArgs& a, long tiles, long slots, int tiles_m, int bn,
+                     std::string& err) {
+  const int nkb = (d.K + kBK - 1) / kBK;
+  a.tail_t0 = (int)tiles;
+  a.tail_parts = 1;
+  a.tail_kbps = nkb;
+  if (a.splits != 1 || !d.out || d.out_bf || d.out_bf_t || tiles <= slots) return 0;
+  const long rem = tiles % slots;
+  if (rem == 0) return 0;
+  int parts = (int)(slots / rem);
+  if (parts > nkb / 4) parts = nkb / 4;           // keep >= 4 k-blocks per part
+  if (parts < 2) return 0;
+  const int kbps = (nkb + parts - 1) / parts;
+  parts = (nkb + kbps - 1) / kbps;
+  if (parts < 2) return 0;
+  a.tail_t0 = (int)(tiles - rem);
+  a.tail_parts = parts;
+  a.tail_kbps = kbps;
+  if (!d.accumulate) {
+    const long col0 = (long)(a.tail_t0 / tiles_m) * bn;
+    const cudaError_t e =
+        d.out_trans ? cudaMemset2DAsync(d.out + col0 * d.ldo, (size_t)d.ldo * 4, 0, (size_t)d.M * 4, (size_t)(d.N - col0),
+                                        c->stream)
+                    : cudaMemset2DAsync(d.out + col0, (size_t)d.ldo * 4, 0, (size_t)(d.N - col0) * 4, (size_t)d.M,
+                                        c->stream);
+    if (e != cudaSuccess) return check_launch("gemm tail memset", err);
+  }
+  return 0;
+}
+
 template <int BN, int STAGES, int BMODE, bool A_MN>
 static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtensorMap& tb,
                   const CUtensorMap& tbs, const CUtensorMap& tea, const CUtensorMap& teb,
@@ -114,6 +148,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
       }
     }
   }
+  if (plan_tail(c, d, a, tiles, (long)c->sm_count, (d.M + kBM - 1) / kBM, BN, err)) return 1;
   // epilogue through TMA stores when the output is a single row-major tensor
   CUtensorMap tout = ta;
   a.tma_out = 0;
@@ -128,7 +163,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
              !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
       a.tma_out = 2;
   }
-  const long items = tiles * a.splits;
+  const long items = a.tail_parts > 1 ? a.tail_t0 + (tiles - a.tail_t0) * a.tail_parts : tiles * a.splits;
   const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
   {
     ProfScope prof_(c, d.name);
@@ -182,7 +217,9 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
       a.tma_out = 2;
   }
   const long tiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + BN - 1) / BN);
-  const long clusters = tiles < (long)max_clusters ? tiles : (long)max_clusters;
+  if (plan_tail(c, d, a, tiles, (long)max_clusters, (d.M + 2 * kBM - 1) / (2 * kBM), BN, err)) return 1;
+  const long items = a.tail_parts > 1 ? a.tail_t0 + (tiles - a.tail_t0) * a.tail_parts : tiles;
+  const long clusters = items < (long)max_clusters ? items : (long)max_clusters;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[2];
   at[0].id = cudaLaunchAttributeClusterDimension;
@@ -314,6 +351,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans; a.bf_scale = d.bf_scale;
   a.out_bf_t = d.out_bf_t; a.ldo_bf_t = d.ldo_bf_t;
   a.tile_cnt = nullptr;
+  a.tail_t0 = 0;
+  a.tail_parts = 1;
+  a.tail_kbps = 0;
   a.err = c->d_err;
   a.splits = 1;
   a.kb_per_split = 1;

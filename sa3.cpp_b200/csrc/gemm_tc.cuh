@@ -54,6 +54,9 @@ struct GemmArgs {
   float* partial;           // split-K: raw f32 partial sums [splits][M][N]; the CTA that finishes a
                             //   tile's last split sums them in split order and runs the epilogue
   int* tile_cnt;            // split-K: per-tile count of finished splits (zero between launches)
+  int tail_t0;              // tail split: tiles [tail_t0, ntiles) (the last, partial round) run as
+  int tail_parts;           //   tail_parts K ranges of tail_kbps k-blocks each, added into the
+  int tail_kbps;            //   output (pre-zeroed unless accumulating); tail_parts <= 1: off
   int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: bf16 `out_bf` via TMA
                             //    store; 0: direct stores (split-K partials, transposed or dual outputs)
   int atomic;               // split-K: every split adds its (scaled) part into `out` with atomics
@@ -61,6 +64,46 @@ struct GemmArgs {
 };
 
 constexpr int kBM = 128, kBK = 64;
+
+// A work item of the persistent GEMM kernels: tile t and its K range [kb0, kb0 + nkb) of 64-wide
+// k-blocks; total adds the K = 16 extension stage to the last range.  Items [0, tail_t0) are
+// whole tiles; with a tail split the remaining tiles are each split into tail_parts ranges
+// (every CTA then gets about the same work); with split-K item = split * ntiles + tile.
+struct WorkItem {
+  int t, kb0, nkb, total;
+  bool first;   // the range that adds the bias
+  bool add;     // tail part: add into the output
+};
+
+template <typename Args>
+__device__ __forceinline__ WorkItem decode_item(const Args& a, int item, int ntiles, int nkb_all) {
+  WorkItem w;
+  bool last;
+  if (a.tail_parts > 1 && item >= a.tail_t0) {
+    const int j = item - a.tail_t0, part = j % a.tail_parts;
+    w.t = a.tail_t0 + j / a.tail_parts;
+    w.kb0 = part * a.tail_kbps;
+    w.nkb = min(nkb_all - w.kb0, a.tail_kbps);
+    w.first = part == 0;
+    last = part == a.tail_parts - 1;
+    w.add = true;
+  } else {
+    const int split = item / ntiles;
+    w.t = item % ntiles;
+    w.kb0 = split * a.kb_per_split;
+    w.nkb = min(nkb_all - w.kb0, a.kb_per_split);
+    w.first = split == 0;
+    last = split == a.splits - 1;
+    w.add = false;
+  }
+  w.total = w.nkb + ((a.has_ext && last) ? 1 : 0);
+  return w;
+}
+
+template <typename Args>
+__device__ __forceinline__ int num_items(const Args& a, int ntiles) {
+  return a.tail_parts > 1 ? a.tail_t0 + (ntiles - a.tail_t0) * a.tail_parts : ntiles * a.splits;
+}
 // the K = 16 extension's A tile: 128 rows of u^T as two 64 (M) x 16 (K) MN-major boxes
 constexpr int kExtABytes = 128 * 16 * 2;
 
@@ -343,16 +386,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
   const int tiles_m = (args.M + kBM - 1) / kBM;
   const int tiles_n = (args.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
-  const int nitems = ntiles * args.splits;
+  const int nitems = num_items(args, ntiles);
   const int nkb_all = (args.K + kBK - 1) / kBK;   // a ragged last block reads TMA zero fill
-  // item -> (tile, split); split s covers k-blocks [s*kps, min(nkb_all, (s+1)*kps)) and the last
-  // split also runs the K = 16 extension
-  auto item_kb = [&](int item, int& kb0, int& nkb, int& total) {
-    const int split = item / ntiles;
-    kb0 = split * args.kb_per_split;
-    nkb = min(nkb_all - kb0, args.kb_per_split);
-    total = nkb + ((args.has_ext && split == args.splits - 1) ? 1 : 0);
-  };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -404,10 +439,9 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-        const int t = item % ntiles;
-        const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
-        int kb0, nkb, total;
-        item_kb(item, kb0, nkb, total);
+        const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+        const int m0 = (w.t % tiles_m) * kBM, n0 = (w.t / tiles_m) * BN;
+        const int kb0 = w.kb0, nkb = w.nkb, total = w.total;
         for (int kb = 0; kb < total; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
@@ -474,8 +508,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     int it = 0, ti = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++ti) {
-      int kb0, nkb, total;
-      item_kb(item, kb0, nkb, total);
+      const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+      const int nkb = w.nkb, total = w.total;
       const int a = ti & 1;
       const uint32_t ause = (uint32_t)(ti >> 1);
       if (ti >= 2 && !wt(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
@@ -518,7 +552,11 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     int nstore = 0;
     int ti = 0;
     for (int item = blockIdx.x; item < nitems; item += gridDim.x, ++ti) {
-      const int t = item % ntiles;
+      const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+      const int t = w.t;
+      // parts of a split tile add into the output; only the first part adds the bias
+      const bool add = w.add || args.atomic;
+      const float* bias = (w.first || !add) ? args.col_bias : nullptr;
       const int a = ti & 1;
       const uint32_t ause = (uint32_t)(ti >> 1);
       const int m0 = (t % tiles_m) * kBM, n0 = (t / tiles_m) * BN;
@@ -541,9 +579,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             tmem_ld16(tacc + (uint32_t)cc, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
           }
           tmem_ld_wait();
-          // with atomic split-K every split adds its scaled part; only split 0 adds the bias
-          epi_columns(v, f + 32 * h, nb + 32 * h, args, split_out,
-                      (args.atomic && item >= ntiles) ? nullptr : args.col_bias);
+          epi_columns(v, f + 32 * h, nb + 32 * h, args, split_out, bias);
         }
         if (!have || nb >= args.N) continue;
         if (args.tma_out) {
@@ -576,7 +612,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (args.accumulate) tma_reduce_add_2d(&tm_out, buf, nb, rbase);
+            if (args.accumulate || w.add) tma_reduce_add_2d(&tm_out, buf, nb, rbase);
             else tma_store_2d(&tm_out, buf, nb, rbase);
             bulk_commit();
           }
@@ -592,7 +628,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             if (j >= ncols) break;
             if (args.out && args.out_trans) {
               float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
-              if (args.atomic) atomicAdd(dst, f[j]);
+              if (add) atomicAdd(dst, f[j]);
               else *dst = args.accumulate ? *dst + f[j] : f[j];
             }
             if (args.out_bf && args.out_bf_trans)
@@ -626,7 +662,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
             }
             if (args.out && !args.out_trans) {
               float* dst = args.out + (long)row * args.ldo + nb + lane;
-              if (args.atomic) atomicAdd(dst, x);
+              if (add) atomicAdd(dst, x);
               else *dst = args.accumulate ? *dst + x : x;
             }
             if (args.out_bf && !args.out_bf_trans)
@@ -669,8 +705,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
       int it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x) {
-        int kb0, nkb, total;
-        item_kb(item, kb0, nkb, total);
+        const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+        const int nkb = w.nkb, total = w.total;
         for (int kb = 0; kb < total; ++kb, ++it) {
           // Every stage use is observed (and acknowledged on bready), the extension stage too
           // (it is loaded as bf16 by TMA and needs no work): skipping a phase would make the

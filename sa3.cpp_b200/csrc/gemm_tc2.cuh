@@ -148,8 +148,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int tiles_m = (args.M + PM - 1) / PM;
   const int tiles_n = (args.N + BN - 1) / BN;
   const int ntiles = tiles_m * tiles_n;
-  const int nkb = (args.K + kBK - 1) / kBK;
-  const int total = nkb + (args.has_ext ? 1 : 0);
+  const int nkb_all = (args.K + kBK - 1) / kBK;
+  const int nitems = num_items(args, ntiles);   // work items over pair tiles (gemm_tc.cuh)
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -201,9 +201,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const uint32_t full0 = mapa_shared(smem_u32(full), 0);   // the even CTA's full[0]
       int it = 0;
       bool ok = true;
-      for (int t = cluster; t < ntiles && ok; t += nclusters) {
-        const int m0 = (t % tiles_m) * PM + (int)rank * kBM;
-        const int n0 = (t / tiles_m) * BN + (int)rank * L::BH;
+      for (int item = cluster; item < nitems && ok; item += nclusters) {
+        const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+        const int m0 = (w.t % tiles_m) * PM + (int)rank * kBM;
+        const int n0 = (w.t / tiles_m) * BN + (int)rank * L::BH;
+        const int nkb = w.nkb, total = w.total;
         for (int kb = 0; kb < total; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);
@@ -214,7 +216,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (leader)
             mbar_arrive_expect_tx(&full[s], 2u * (uint32_t)((kb < nkb ? L::A_BYTES : kExtABytes) + L::B_BYTES));
           if (kb < nkb) {
-            const int k0 = kb * kBK;
+            const int k0 = (w.kb0 + kb) * kBK;
             tma_load_2d_pair(a_st, &tm_a, fb, k0, m0);
             if (!BMN) {
               tma_load_2d_pair(b_st, &tm_b, fb, k0, n0);
@@ -245,7 +247,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       constexpr uint32_t B_KSTEP = BMN ? 2048 >> 4 : 32 >> 4;
       int it = 0, ti = 0;
       bool ok = true;
-      for (int t = cluster; t < ntiles && ok; t += nclusters, ++ti) {
+      for (int item = cluster; item < nitems && ok; item += nclusters, ++ti) {
+        const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+        const int nkb = w.nkb, total = w.total;
         const int a = ti & 1;
         const uint32_t ause = (uint32_t)(ti >> 1);
         if (ti >= 2 && !wt(&tempty[a], (ause & 1u) ^ 1u, kErrTimeoutOther)) { ok = false; break; }
@@ -279,7 +283,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     const int cstep = args.tma_out == 2 ? 64 : 32;
     const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
     int nstore = 0, ti = 0;
-    for (int t = cluster; t < ntiles; t += nclusters, ++ti) {
+    for (int item = cluster; item < nitems; item += nclusters, ++ti) {
+      const WorkItem w = decode_item(args, item, ntiles, nkb_all);
+      const int t = w.t;
+      const float* bias = w.first ? args.col_bias : nullptr;   // tail parts: the first adds the bias
       const int a = ti & 1;
       const uint32_t ause = (uint32_t)(ti >> 1);
       const int m0 = (t % tiles_m) * PM + (int)rank * kBM, n0 = (t / tiles_m) * BN;
@@ -297,7 +304,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           uint32_t v[32];
           tmem_ld32(tacc + (uint32_t)(c0 + 32 * h), v);
           tmem_ld_wait();
-          epi_columns(v, f + 32 * h, nb + 32 * h, args, false, args.col_bias);
+          epi_columns(v, f + 32 * h, nb + 32 * h, args, false, bias);
         }
         if (!have || nb >= args.N) continue;
         if (args.tma_out) {
@@ -328,7 +335,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            if (args.accumulate) tma_reduce_add_2d(&tm_out, buf, nb, rbase);
+            if (args.accumulate || w.add) tma_reduce_add_2d(&tm_out, buf, nb, rbase);
             else tma_store_2d(&tm_out, buf, nb, rbase);
             bulk_commit();
           }
@@ -344,7 +351,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             for (int j = 0; j < 32; ++j) {   // static indices keep f[] in registers
               if (j >= ncols) break;
               float* dst = args.out + (long)(nb + j) * args.ldo + myrow;
-              *dst = args.accumulate ? *dst + f[j] : f[j];
+              if (w.add) atomicAdd(dst, f[j]);
+              else *dst = args.accumulate ? *dst + f[j] : f[j];
             }
           }
         }
@@ -368,7 +376,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             const float x = st32[r * 32 + (lane ^ r)];
             if (args.out && !args.out_trans) {
               float* dst = args.out + (long)row * args.ldo + nb + lane;
-              *dst = args.accumulate ? *dst + x : x;
+              if (w.add) atomicAdd(dst, x);
+              else *dst = args.accumulate ? *dst + x : x;
             }
             if (args.out_bf && !args.out_bf_trans) args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x);
           }

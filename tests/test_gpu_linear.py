@@ -168,7 +168,8 @@ def _outputs(ctx, c, qtype, S, inn, out, rank):
 def test_cta_pair_gemms_match_single_cta(ctx, S, inn, out):
     """The forward and dX GEMMs of these shapes run on CTA pairs (cta_group::2, 256-row tiles) by
     default; with pairs switched off they run one CTA per 128-row tile.  Both accumulate every
-    output element over K in the same order, so y and dx agree to f32 rounding (and the adapter
+    output element over K in the same order (except the tiles of a last, partial round, which may
+    run as K parts added into the output), so y and dx agree to f32 rounding (and the adapter
     gradients, fed by them, to the rounding of their atomic column sums)."""
     import sa3k
     c = _case("q8_0", S, inn, out, 16, 31)
@@ -179,7 +180,7 @@ def test_cta_pair_gemms_match_single_cta(ctx, S, inn, out):
     ctx.set_option(sa3k.OPT_GEMM_PAIR, 1)
     for k in ("y", "dx"):
         assert np.isfinite(got[1][k]).all(), k
-        assert rel_l2(got[1][k], got[0][k]) < 1e-6, k
+        assert rel_l2(got[1][k], got[0][k]) < 1e-5, k     # K parts of tail tiles reassociate the f32 sums
     for k in ("dA", "dB", "dm"):
         assert rel_l2(got[1][k], got[0][k]) < 1e-5, k
     if S * inn * out <= 1e10:     # oracle check where the float64 restatement stays quick
@@ -189,6 +190,28 @@ def test_cta_pair_gemms_match_single_cta(ctx, S, inn, out):
                "dA": rel_l2(got[1]["dA"], ref["dA"]), "dB": rel_l2(got[1]["dB"], ref["dB"]),
                "dm": rel_l2(got[1]["dm"], ref["dm"])}
         assert all(v < TOL for v in res.values()), res
+
+
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_tail_split_gemms_match_oracle(ctx, accumulate):
+    """4352 token rows, 1536 -> 1536: the dX GEMM has 102 256 x 256 pair tiles for 74 CTA pairs,
+    so its last, partial round runs as two K halves per tile added into dx (zeroed first, or the
+    existing dx when accumulating); every other output goes through the whole-tile path."""
+    import torch
+    S, inn, out = 4352, 1536, 1536
+    c = _case("q8_0", S, inn, out, 16, 41)
+    w = ctx.upload(c["raw"], "q8_0", inn, out)
+    x, dy = _dev(c["x"]), _dev(c["dy"])
+    y = torch.empty(S, out, device="cuda")
+    ctx.linear_fwd(w, x, y)
+    dx0 = torch.randn(S, inn, device="cuda") if accumulate else torch.zeros(S, inn, device="cuda")
+    dx = dx0.clone()
+    ctx.linear_bwd(w, x, y, dy, dx, accumulate=accumulate)
+    ctx.sync()
+    ref_y, cache = oracle.dit_lin_fwd(c["x"], c["Wd"], None, None, 1.0, None, None, None)
+    ref = oracle.dit_lin_bwd(c["dy"], cache)
+    assert rel_l2(y.cpu().numpy(), ref_y) < TOL
+    assert rel_l2((dx - dx0).cpu().numpy(), ref["dx"]) < TOL
 
 
 def test_linear_accumulate(ctx):
