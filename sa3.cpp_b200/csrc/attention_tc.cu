@@ -109,6 +109,39 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   return d;
 }
 
+__device__ __forceinline__ uint64_t fadd2_rm(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rm.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x for two values on the FMA / integer pipes instead of the MUFU unit (part of the softmax
+// exponentials run here so that both kinds of pipe share the work).  Method: Cody-Waite range
+// reduction x = n + f with n = floor(x) (x + 1.5 * 2^23 rounded toward -inf leaves n in the low
+// mantissa bits) and f in [0, 1), a degree-3 polynomial for 2^f fitted here by iteratively
+// reweighted least squares for minimax relative error (< 8e-5 on [0, 1)), and n added into the
+// exponent field.  x is clamped to >= -125, so arguments below give ~2^-125 instead of 0 (far
+// below what the bf16 P or the f32 row sum register).
+// which pairs of every 8 take ex2_poly2 (3 of 8: the MUFU and FMA pipes then finish together)
+__device__ constexpr bool kPolyPair[8] = {true, false, false, true, false, true, false, false};
+
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  constexpr float kMagic = 12582912.0f;   // 1.5 * 2^23
+  const uint64_t x = f2(fmaxf(x0, -125.f), fmaxf(x1, -125.f));
+  const uint64_t t = fadd2_rm(x, f2(kMagic, kMagic));           // kMagic + floor(x), exact
+  const uint64_t n = fadd2(t, f2(-kMagic, -kMagic));             // floor(x)
+  const uint64_t fr = ffma2(n, f2(-1.f, -1.f), x);               // x - floor(x), in [0, 1)
+  uint64_t p = ffma2(f2(0.07802403f, 0.07802403f), fr, f2(0.22606707f, 0.22606707f));
+  p = ffma2(p, fr, f2(0.69583398f, 0.69583398f));
+  p = ffma2(p, fr, f2(0.99992514f, 0.99992514f));
+  float p0, p1, t0, t1;
+  f2split(p, p0, p1);
+  f2split(t, t0, t1);
+  const int mb = __float_as_int(kMagic);
+  y0 = __int_as_float(__float_as_int(p0) + ((__float_as_int(t0) - mb) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + ((__float_as_int(t1) - mb) << 23));
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -383,7 +416,13 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             float x0, x1;
             f2split(ffma2(f2(__uint_as_float(v[32 * c + 2 * e]), __uint_as_float(v[32 * c + 2 * e + 1])), sc2, nb2),
                     x0, x1);
-            const float p0 = ex2(x0), p1 = ex2(x1);
+            float p0, p1;
+            if (kPolyPair[e & 7]) {      // a share of the exponentials on the FMA pipes
+              ex2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
             lsum[e & 1] = fadd2(lsum[e & 1], f2(p0, p1));
             pk[e] = pack_bf16x2(p0, p1);
           }
