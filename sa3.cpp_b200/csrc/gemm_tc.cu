@@ -122,9 +122,12 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   a.splits = 1;
   a.kb_per_split = nkb > 0 ? nkb : 1;
   a.partial = nullptr;
-  if (tiles * 2 <= (long)c->sm_count && nkb >= 8) {
+  // (splits that end in the in-kernel reduction keep >= 16 k-blocks each: below that the
+  // reduction by the last CTA of a tile costs more than the shorter K loop saves)
+  const int min_kb = (d.atomic_split && d.out && !d.out_bf) ? 4 : 16;
+  if (tiles * 2 <= (long)c->sm_count && nkb >= 2 * min_kb) {
     int splits = (int)((long)c->sm_count / tiles);
-    if (splits > nkb / 4) splits = nkb / 4;        // keep >= 4 k-blocks per split
+    if (splits > nkb / min_kb) splits = nkb / min_kb;
     if (splits > 1) {
       const int kps = (nkb + splits - 1) / splits;
       splits = (nkb + kps - 1) / kps;
