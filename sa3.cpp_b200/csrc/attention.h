@@ -59,13 +59,18 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
 // forward input y and the saved rstd.
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& s,
                     int tokens_per_sample, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf,
-                    std::string& err);
-// Self-attention q/k/v head preparation backward (dq3 = [dq | dk | dv] f32, qkv = the projection
-// output) fused with the qkv projection's backward prologue: dz = bf16(g * dy) [T][3D] and
-// dg[3D] = colsum(dy * qkv / g) (DoRA g; null: plain bf16 conversion, dg untouched).
-int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, const float* rq, const float* rk,
-                 const float* gq, const float* gk, int tokens_per_sample, int rot, float rope_base, const float* g,
+                    std::string& err, float gscale = 1.0f);   // g enters multiplied by gscale
+// Self-attention q/k/v head preparation backward (dq3 = [dq | dk | dv] f32, or with nsl = 5 the
+// differential layout [dq | dk | dv | dqd | dkd] whose second stream ran on +dO, dv2 its dV, and
+// rq2 / rk2 its rstd; qkv = the projection output) fused with the qkv projection's backward
+// prologue: dz = bf16(g * dy) [T][nsl D] and dg = colsum(dy * qkv / g) (DoRA g; null: plain bf16
+// conversion, dg untouched).
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, int nsl, const float* rq,
+                 const float* rk, const float* rq2, const float* rk2, const float* dv2, const float* gq,
+                 const float* gk, int tokens_per_sample, int rot, float rope_base, const float* g,
                  __nv_bfloat16* dz, float* dg, std::string& err);
+// out = x - y (bf16, n a multiple of 8)
+int k_sub_bf16(Ctx* c, const __nv_bfloat16* x, const __nv_bfloat16* y, long n, __nv_bfloat16* out, std::string& err);
 
 // x_out = x_in + y * gate[sample]  (gate already sigmoid(1 - g)); x_out may alias x_in
 int k_gate_residual(Ctx* c, const float* x_in, const float* y, const float* gate, long gate_stride, int T, int D,

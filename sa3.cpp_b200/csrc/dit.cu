@@ -26,6 +26,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -55,6 +56,10 @@ struct DitBlockAct {
   float* mod = nullptr;
   __nv_bfloat16 *h_a = nullptr, *qkvb = nullptr, *oa = nullptr, *hc = nullptr, *cq = nullptr, *kvb = nullptr;
   __nv_bfloat16 *oc = nullptr, *hf = nullptr, *act = nullptr;
+  // differential attention: both softmax streams' outputs (oa = o1 - o2, oc = oc1 - oc2), the
+  // second stream's log-sum-exp and the rstd of its q / k heads (null otherwise)
+  __nv_bfloat16 *o1 = nullptr, *o2 = nullptr, *oc1 = nullptr, *oc2 = nullptr;
+  float *lse_a2 = nullptr, *lse_c2 = nullptr, *rq2 = nullptr, *rk2 = nullptr, *rcq2 = nullptr;
   __nv_bfloat16* ut[4] = {nullptr, nullptr, nullptr, nullptr};
 };
 
@@ -101,6 +106,7 @@ struct DitModel {
   float *pout = nullptr, *vel = nullptr, *dvel = nullptr, *loss = nullptr, *dp = nullptr, *dxT = nullptr;
   // backward temporaries
   float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dact = nullptr, *dq3 = nullptr, *Dsum = nullptr;
+  float* dv2 = nullptr;   // differential: dV of the second softmax stream (run on +dO)
   __nv_bfloat16* dO_b = nullptr;
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
@@ -117,6 +123,8 @@ struct DitModel {
 
   int Sfull() const { return cfg.mem_tokens + T; }
   int qkv_cols() const { return (cfg.differential ? 5 : 3) * cfg.dim; }
+  int cq_cols() const { return (cfg.differential ? 2 : 1) * cfg.dim; }    // cross.q output
+  int ckv_cols() const { return (cfg.differential ? 3 : 2) * cfg.dim; }   // cross.kv output
   std::string bname(int l, const char* suffix) const { return "dit." + std::to_string(l) + "." + suffix; }
   const Weight* weight(const std::string& n, std::string& err) const {
     auto it = W.find(n);
@@ -228,6 +236,8 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
   m.B = B; m.T = T; m.C = C;
   const int64_t S = m.Sfull(), M = (int64_t)B * S, D = k.dim, Hh = k.heads, I = k.ff_inner;
   const int64_t Q = m.qkv_cols(), MC = (int64_t)B * C, MT = (int64_t)B * T;
+  const int64_t Dq = m.cq_cols(), Dk = m.ckv_cols();
+  const bool diff = k.differential != 0;
   m.ut_ld = (M + 63) / 64 * 64;
   // two passes: measure, then carve
   for (int pass = 0; pass < 2; ++pass) {
@@ -245,8 +255,12 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       DitBlockAct& a = m.blk[l];
       a.x = f(M * D); a.rstd_a = f(M); a.h_a = h(M * D); a.qkv = f(M * Q); a.qkvb = h(M * Q);
       a.rq = f(M * Hh); a.rk = f(M * Hh); a.oa = h(M * D); a.lse_a = f(B * Hh * S); a.yo = f(M * D);
-      a.x1 = f(M * D); a.rstd_c = f(M); a.hc = h(M * D); a.qf = f(M * D); a.cq = h(M * D); a.rcq = f(M * Hh);
-      a.kvf = f(MC * 2 * D); a.kvb = h(MC * 2 * D); a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
+      a.x1 = f(M * D); a.rstd_c = f(M); a.hc = h(M * D); a.qf = f(M * Dq); a.cq = h(M * Dq); a.rcq = f(M * Hh);
+      a.kvf = f(MC * Dk); a.kvb = h(MC * Dk); a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
+      if (diff) {
+        a.o1 = h(M * D); a.o2 = h(M * D); a.oc1 = h(M * D); a.oc2 = h(M * D);
+        a.lse_a2 = f(B * Hh * S); a.lse_c2 = f(B * Hh * S); a.rq2 = f(M * Hh); a.rk2 = f(M * Hh); a.rcq2 = f(M * Hh);
+      }
       a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = f(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
       a.mod = f(B * 6 * D);
       for (int j = 0; j < 4; ++j) a.ut[j] = h(16 * m.ut_ld);
@@ -264,6 +278,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     const int64_t wide = std::max<int64_t>(std::max<int64_t>(Q, 2 * I), D);
     m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact = f(M * I); m.dq3 = f(M * Q);
     m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
+    m.dv2 = diff ? f(M * D) : nullptr;
     const int64_t maxout = std::max<int64_t>(wide, 6 * D);
     m.dg = f(maxout); m.c3 = f(256);
     m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
@@ -340,6 +355,34 @@ static DitTarget* target(DitModel& m, const std::string& name) {
   return it == m.tix.end() ? nullptr : &m.tg[(size_t)it->second];
 }
 
+// self-attention of block `a` over the prepared [q | k | v (| qd | kd)] rows: softmax stream 0
+// (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] bf16
+static AttnArgs self_attn(const DitBlockAct& a, int B, int H, int S, int D, int Q, float scale, int st,
+                          __nv_bfloat16* o) {
+  AttnArgs r;
+  r.B = B; r.H = H; r.Sq = S; r.Sk = S; r.scale = scale; r.window = -1;
+  r.q = a.qkvb + (st ? 3 * D : 0); r.q_sb = (long)S * Q; r.q_sh = 64; r.q_ld = Q;
+  r.k = a.qkvb + (st ? 4 * D : D); r.k_sb = r.q_sb; r.k_sh = 64; r.k_ld = Q;
+  r.v = a.qkvb + 2 * D; r.v_sb = r.q_sb; r.v_sh = 64; r.v_ld = Q;
+  r.o = o; r.o_sb = (long)S * D; r.o_sh = 64; r.o_ld = D;
+  r.lse = st ? a.lse_a2 : a.lse_a;
+  return r;
+}
+
+// cross-attention of block `a`: queries [cq (| cqd)] [M][Dq], context rows [ck (| ckd) | cv]
+// [B C][Dk]; stream st as for self_attn
+static AttnArgs cross_attn(const DitBlockAct& a, int B, int H, int S, int C, int D, int Dq, int Dk, float scale,
+                           int st, __nv_bfloat16* o) {
+  AttnArgs r;
+  r.B = B; r.H = H; r.Sq = S; r.Sk = C; r.scale = scale; r.window = -1;
+  r.q = a.cq + st * D; r.q_sb = (long)S * Dq; r.q_sh = 64; r.q_ld = Dq;
+  r.k = a.kvb + st * D; r.k_sb = (long)C * Dk; r.k_sh = 64; r.k_ld = Dk;
+  r.v = a.kvb + (Dk - D); r.v_sb = r.k_sb; r.v_sh = 64; r.v_ld = Dk;
+  r.o = o; r.o_sb = (long)S * D; r.o_sh = 64; r.o_ld = D;
+  r.lse = st ? a.lse_c2 : a.lse_c;
+  return r;
+}
+
 // ------------------------------------------------------------------ forward + backward
 static int dit_step(DitModel& m, std::string& err) {
   Ctx* c = m.c;
@@ -348,7 +391,8 @@ static int dit_step(DitModel& m, std::string& err) {
   const int64_t M = (int64_t)B * S, MT = (int64_t)B * T, MC = (int64_t)B * C;
   const int Q = m.qkv_cols();
   const float scale = 1.0f / std::sqrt((float)k.head_dim);
-  if (k.differential) { err = "differential attention is not supported by the training step yet"; return 1; }
+  const bool diff = k.differential != 0;
+  const int Dq = m.cq_cols(), Dk = m.ckv_cols();
 
   // adapters: operand forms + DoRA norms, once per step (grouped launches over all adapters; the
   // DoRA P = W A^T GEMMs run per adapter between them)
@@ -419,45 +463,54 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err)) return 1;
     if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, a.ut[0], err)) return 1;
     {
-      HeadSlice hs[3];
+      // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE
+      HeadSlice hs[5];
       hs[0].col = 0; hs[0].gamma = g_q; hs[0].rope = 1; hs[0].rstd = a.rq;
       hs[1].col = D; hs[1].gamma = g_k; hs[1].rope = 1; hs[1].rstd = a.rk;
       hs[2].col = 2 * D;
-      if (k_head_prep_fwd(c, a.qkv, (int)M, Q, H, hs, 3, S, k.qk_eps, k.rot, k.rope_base, a.qkvb, err)) return 1;
+      hs[3].col = 3 * D; hs[3].gamma = g_q; hs[3].rope = 1; hs[3].rstd = a.rq2;
+      hs[4].col = 4 * D; hs[4].gamma = g_k; hs[4].rope = 1; hs[4].rstd = a.rk2;
+      if (k_head_prep_fwd(c, a.qkv, (int)M, Q, H, hs, diff ? 5 : 3, S, k.qk_eps, k.rot, k.rope_base, a.qkvb, err))
+        return 1;
     }
-    AttnArgs sa;
-    sa.B = B; sa.H = H; sa.Sq = S; sa.Sk = S; sa.scale = scale; sa.window = -1;
-    sa.q = a.qkvb; sa.q_sb = (long)S * Q; sa.q_sh = 64; sa.q_ld = Q;
-    sa.k = a.qkvb + D; sa.k_sb = sa.q_sb; sa.k_sh = 64; sa.k_ld = Q;
-    sa.v = a.qkvb + 2 * D; sa.v_sb = sa.q_sb; sa.v_sh = 64; sa.v_ld = Q;
-    sa.o = a.oa; sa.o_sb = (long)S * D; sa.o_sh = 64; sa.o_ld = D;
-    sa.lse = a.lse_a;
+    AttnArgs sa = self_attn(a, B, H, S, D, Q, scale, 0, diff ? a.o1 : a.oa);
     if (attn_forward(c, sa, err)) return 1;
+    if (diff) {
+      // differential attention (src/dit.h:152-158): o = sdpa(q, k, v) - sdpa(qd, kd, v)
+      AttnArgs sd = self_attn(a, B, H, S, D, Q, scale, 1, a.o2);
+      if (attn_forward(c, sd, err)) return 1;
+      if (k_sub_bf16(c, a.o1, a.o2, M * D, a.oa, err)) return 1;
+    }
     if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, a.ut[1], err)) return 1;
     if (k_gate_residual(c, a.x, a.yo, a.mod + 2 * D, ms, (int)M, D, S, a.x1, err)) return 1;
     // cross-attention branch
     if (k_rmsnorm_mod_fwd(c, a.x1, (int)M, D, g_cn, nullptr, nullptr, 0, S, k.norm_eps, a.hc, a.rstd_c, err)) return 1;
     if (lin_fwd(m, wcq, nullptr, nullptr, a.hc, M, a.qf, nullptr, nullptr, err)) return 1;
     {
-      HeadSlice hs;
-      hs.col = 0; hs.gamma = g_cq; hs.rstd = a.rcq;
-      if (k_head_prep_fwd(c, a.qf, (int)M, D, H, &hs, 1, S, k.qk_eps, k.rot, k.rope_base, a.cq, err)) return 1;
+      // [cq (| cqd)], both with cross.q_norm, no RoPE
+      HeadSlice hs[2];
+      hs[0].col = 0; hs[0].gamma = g_cq; hs[0].rstd = a.rcq;
+      hs[1].col = D; hs[1].gamma = g_cq; hs[1].rstd = a.rcq2;
+      if (k_head_prep_fwd(c, a.qf, (int)M, Dq, H, hs, diff ? 2 : 1, S, k.qk_eps, k.rot, k.rope_base, a.cq, err))
+        return 1;
     }
     if (lin_fwd(m, wckv, nullptr, nullptr, m.context_b, MC, a.kvf, nullptr, nullptr, err)) return 1;
     {
-      HeadSlice hs[2];
-      hs[0].col = 0; hs[0].gamma = g_ck; hs[0].rstd = a.rck;
-      hs[1].col = D;
-      if (k_head_prep_fwd(c, a.kvf, (int)MC, 2 * D, H, hs, 2, C, k.qk_eps, k.rot, k.rope_base, a.kvb, err)) return 1;
+      // [ck (| ckd) | cv], ck / ckd with cross.k_norm (the context side is frozen: no rstd kept)
+      HeadSlice hs[3];
+      hs[0].col = 0; hs[0].gamma = g_ck;
+      if (diff) { hs[1].col = D; hs[1].gamma = g_ck; }
+      hs[diff ? 2 : 1].col = Dk - D;
+      if (k_head_prep_fwd(c, a.kvf, (int)MC, Dk, H, hs, diff ? 3 : 2, C, k.qk_eps, k.rot, k.rope_base, a.kvb, err))
+        return 1;
     }
-    AttnArgs ca;
-    ca.B = B; ca.H = H; ca.Sq = S; ca.Sk = C; ca.scale = scale; ca.window = -1;
-    ca.q = a.cq; ca.q_sb = (long)S * D; ca.q_sh = 64; ca.q_ld = D;
-    ca.k = a.kvb; ca.k_sb = (long)C * 2 * D; ca.k_sh = 64; ca.k_ld = 2 * D;
-    ca.v = a.kvb + D; ca.v_sb = ca.k_sb; ca.v_sh = 64; ca.v_ld = 2 * D;
-    ca.o = a.oc; ca.o_sb = (long)S * D; ca.o_sh = 64; ca.o_ld = D;
-    ca.lse = a.lse_c;
+    AttnArgs ca = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, 0, diff ? a.oc1 : a.oc);
     if (attn_forward(c, ca, err)) return 1;
+    if (diff) {
+      AttnArgs cd = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, 1, a.oc2);
+      if (attn_forward(c, cd, err)) return 1;
+      if (k_sub_bf16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
+    }
     if (lin_fwd(m, wco, nullptr, nullptr, a.oc, M, m.dtmp, nullptr, nullptr, err)) return 1;
     if (k_add(c, a.x1, m.dtmp, (long)M * D, a.x2, err)) return 1;
     // feed-forward branch
@@ -513,22 +566,20 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, m.dz, err)) return 1;
     // cross-attention branch (context and its projections are frozen: only dq flows)
     if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, nullptr, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
-    {
-      AttnArgs ca;
-      ca.B = B; ca.H = H; ca.Sq = S; ca.Sk = C; ca.scale = scale; ca.window = -1;
-      ca.q = a.cq; ca.q_sb = (long)S * D; ca.q_sh = 64; ca.q_ld = D;
-      ca.k = a.kvb; ca.k_sb = (long)C * 2 * D; ca.k_sh = 64; ca.k_ld = 2 * D;
-      ca.v = a.kvb + D; ca.v_sb = ca.k_sb; ca.v_sh = 64; ca.v_ld = 2 * D;
-      ca.o = a.oc; ca.o_sb = (long)S * D; ca.o_sh = 64; ca.o_ld = D;
-      ca.lse = a.lse_c;
+    for (int st = 0; st < (diff ? 2 : 1); ++st) {
+      // stream st's dq into m.dtmp [M][Dq] columns st D.. (the second differential stream runs on
+      // +dO, so its gradient enters the head backward negated)
+      AttnArgs ca = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, st, st ? a.oc2 : diff ? a.oc1 : a.oc);
       ca.dO = m.dO_b; ca.dO_sb = (long)S * D; ca.dO_sh = 64; ca.dO_ld = D;
       ca.Dsum = m.Dsum;
-      ca.dq = m.dtmp; ca.dq_sb = (long)S * D; ca.dq_sh = 64; ca.dq_ld = D;
+      ca.dq = m.dtmp + st * D; ca.dq_sb = (long)S * Dq; ca.dq_sh = 64; ca.dq_ld = Dq;
       if (attn_backward(c, ca, false, err)) return 1;
       HeadSlice hs;
-      hs.col = 0; hs.gamma = g_cq; hs.rstd = a.rcq;
+      hs.col = st * D; hs.gamma = g_cq; hs.rstd = st ? a.rcq2 : a.rcq;
       // bf16 gradient straight into m.dz: the input of the cross.q backward
-      if (k_head_prep_bwd(c, m.dtmp, D, a.qf, (int)M, D, H, hs, S, k.rot, k.rope_base, nullptr, m.dz, err)) return 1;
+      if (k_head_prep_bwd(c, m.dtmp + st * D, Dq, a.qf, (int)M, Dq, H, hs, S, k.rot, k.rope_base, nullptr, m.dz, err,
+                          st ? -1.0f : 1.0f))
+        return 1;
     }
     if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, nullptr, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, nullptr, err)) return 1;
@@ -537,25 +588,26 @@ static int dit_step(DitModel& m, std::string& err) {
                       to && to->prep.dora() ? to->prep.g : nullptr, dz_of(m, to), dg_of(m, to), err))
       return 1;
     if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, nullptr, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
-    {
-      AttnArgs sa;
-      sa.B = B; sa.H = H; sa.Sq = S; sa.Sk = S; sa.scale = scale; sa.window = -1;
-      sa.q = a.qkvb; sa.q_sb = (long)S * Q; sa.q_sh = 64; sa.q_ld = Q;
-      sa.k = a.qkvb + D; sa.k_sb = sa.q_sb; sa.k_sh = 64; sa.k_ld = Q;
-      sa.v = a.qkvb + 2 * D; sa.v_sb = sa.q_sb; sa.v_sh = 64; sa.v_ld = Q;
-      sa.o = a.oa; sa.o_sb = (long)S * D; sa.o_sh = 64; sa.o_ld = D;
-      sa.lse = a.lse_a;
+    for (int st = 0; st < (diff ? 2 : 1); ++st) {
+      // m.dq3 [M][Q] = [dq | dk | dv (| dqd' | dkd')]: the second differential stream runs on +dO
+      // and leaves its (negated) q / k gradients in the last two slices and its dV in m.dv2
+      AttnArgs sa = self_attn(a, B, H, S, D, Q, scale, st, st ? a.o2 : diff ? a.o1 : a.oa);
       sa.dO = m.dO_b; sa.dO_sb = (long)S * D; sa.dO_sh = 64; sa.dO_ld = D;
       sa.Dsum = m.Dsum;
-      sa.dq = m.dq3; sa.dq_sb = (long)S * Q; sa.dq_sh = 64; sa.dq_ld = Q;
-      sa.dk = m.dq3 + D; sa.dk_sb = sa.dq_sb; sa.dk_sh = 64; sa.dk_ld = Q;
-      sa.dv = m.dq3 + 2 * D; sa.dv_sb = sa.dq_sb; sa.dv_sh = 64; sa.dv_ld = Q;
+      sa.dq = m.dq3 + (st ? 3 * D : 0); sa.dq_sb = (long)S * Q; sa.dq_sh = 64; sa.dq_ld = Q;
+      sa.dk = m.dq3 + (st ? 4 * D : D); sa.dk_sb = sa.dq_sb; sa.dk_sh = 64; sa.dk_ld = Q;
+      if (st) {
+        sa.dv = m.dv2; sa.dv_sb = (long)S * D; sa.dv_sh = 64; sa.dv_ld = D;
+      } else {
+        sa.dv = m.dq3 + 2 * D; sa.dv_sb = sa.dq_sb; sa.dv_sh = 64; sa.dv_ld = Q;
+      }
       if (attn_backward(c, sa, true, err)) return 1;
-      // q / k head preparation backward fused with the qkv projection's prologue
-      if (k_qkv_bwd_dz(c, m.dq3, a.qkv, (int)M, D, H, a.rq, a.rk, g_q, g_k, S, k.rot, k.rope_base,
-                       tq && tq->prep.dora() ? tq->prep.g : nullptr, dz_of(m, tq), dg_of(m, tq), err))
-        return 1;
     }
+    // q / k head preparation backward fused with the qkv projection's prologue
+    if (k_qkv_bwd_dz(c, m.dq3, a.qkv, (int)M, D, H, diff ? 5 : 3, a.rq, a.rk, a.rq2, a.rk2, m.dv2, g_q, g_k, S,
+                     k.rot, k.rope_base, tq && tq->prep.dora() ? tq->prep.g : nullptr, dz_of(m, tq), dg_of(m, tq),
+                     err))
+      return 1;
     if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, nullptr, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, nullptr, err)) return 1;
   }
@@ -581,6 +633,50 @@ using namespace sa3k;
 struct sa3k_dit {
   DitModel m;
 };
+
+// ggml extents (ne0 = the contiguous dimension, ne1 = rows; 1 for vectors) of every tensor the
+// step reads, from the config (the shapes dit_block / dit_head / dit_tail use, src/dit.h:106-147);
+// false for a name the DiT does not have
+static bool dit_tensor_shape(const sa3k_dit_config& k, const std::string& n, int64_t& ne0, int64_t& ne1) {
+  const int64_t D = k.dim, io = k.io, cd = k.cond_dim, td = k.time_dim, I = k.ff_inner;
+  const int64_t dq = k.differential ? 2 : 1;
+  auto set = [&](int64_t a, int64_t b) { ne0 = a; ne1 = b; return true; };
+  static const char* const kPrefix = "dit.";
+  if (n.compare(0, 4, kPrefix) != 0) return false;
+  const std::string r = n.substr(4);
+  if (!r.empty() && r[0] >= '0' && r[0] <= '9') {
+    const size_t dot = r.find('.');
+    if (dot == std::string::npos) return false;
+    const long l = std::strtol(r.substr(0, dot).c_str(), nullptr, 10);
+    if (l < 0 || l >= k.depth) return false;
+    const std::string b = r.substr(dot + 1);
+    if (b == "ssg") return set(6 * D, 1);
+    if (b == "pre_norm.gamma" || b == "cross_norm.gamma" || b == "ff_norm.gamma" || b == "ff.out.bias") return set(D, 1);
+    if (b == "self.q_norm.gamma" || b == "self.k_norm.gamma" || b == "cross.q_norm.gamma" || b == "cross.k_norm.gamma")
+      return set(k.head_dim, 1);
+    if (b == "self.qkv.weight") return set(D, (dq + 1 + dq) * D);
+    if (b == "self.out.weight" || b == "cross.out.weight") return set(D, D);
+    if (b == "cross.q.weight") return set(D, dq * D);
+    if (b == "cross.kv.weight") return set(D, (dq + 1) * D);
+    if (b == "ff.proj.weight") return set(D, 2 * I);
+    if (b == "ff.proj.bias") return set(2 * I, 1);
+    if (b == "ff.out.weight") return set(I, D);
+    return false;
+  }
+  if (r == "time_embed.0.weight") return set(td, D);
+  if (r == "time_embed.0.bias" || r == "time_embed.2.bias" || r == "gce.0.bias") return set(D, 1);
+  if (r == "time_embed.2.weight" || r == "global_embed.2.weight" || r == "gce.0.weight" ||
+      r == "cond_embed.2.weight")
+    return set(D, D);
+  if (r == "global_embed.0.weight" || r == "cond_embed.0.weight") return set(cd, D);
+  if (r == "gce.2.weight") return set(D, 6 * D);
+  if (r == "gce.2.bias") return set(6 * D, 1);
+  if (r == "pre_conv.weight" || r == "post_conv.weight") return set(io, io);
+  if (r == "proj_in.weight") return set(io, D);
+  if (r == "proj_out.weight") return set(D, io);
+  if (r == "memory_tokens") return set(D, k.mem_tokens);
+  return false;
+}
 
 static int dfail(char* err, int len, const std::string& msg) {
   if (err && len > 0) {
@@ -623,6 +719,11 @@ int sa3k_dit_set_tensor(sa3k_dit* d, const char* name, int type, const void* hos
   DitModel& m = d->m;
   cudaSetDevice(m.c->device);
   const std::string n(name);
+  int64_t x0 = 0, x1 = 0;
+  if (!dit_tensor_shape(m.cfg, n, x0, x1)) return dfail(err, err_len, "not a tensor of this DiT: " + n);
+  if (ne0 != x0 || (ne1 > 0 ? ne1 : 1) != x1)
+    return dfail(err, err_len, n + ": shape [" + std::to_string(ne1) + "][" + std::to_string(ne0) + "], expected [" +
+                                   std::to_string(x1) + "][" + std::to_string(x0) + "]");
   const bool is_weight = n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0;
   std::string e;
   if (is_weight) {

@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const float* __restr
 // Backward of one slice.  Grid (ceil(H / 8), ceil(T / kHpRows)).
 __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y,
                                                             int T, int ncols, int H, HeadSlice sl, int tps, int rot,
-                                                            const float2* __restrict__ tab, float* dy,
+                                                            const float2* __restrict__ tab, float gscale, float* dy,
                                                             __nv_bfloat16* dy_bf) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
@@ -238,6 +238,8 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
     float r = 0.f;
     if (valid) {
       ld8(g + (long)t * g_ld + h * 64 + 8 * j, gv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] *= gscale;
       if (sl.gamma) {
         ld8(y + (long)t * ncols + sl.col + h * 64 + 8 * j, yv);
         r = sl.rstd[(long)t * H + h];
@@ -272,11 +274,16 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
 // rms-norm backward; v: identity) fused with the qkv projection's backward prologue: writes
 // dz = bf16(g * dy) and adds colsum(dy * y / g) into dg (DoRA; g null: dz = bf16(dy)), with
 // y = the projection output qkv (no bias).  Block = 8 warps on 8 consecutive head slices of
-// [q heads | k heads | v heads] and kHpRows token rows; each lane adds its 8 columns' dg sums
-// (summed over the warp's four row groups first) once.  Grid (ceil(3H / 8), ceil(T / kHpRows)).
+// [q heads | k heads | v heads (| qd heads | kd heads)] and kHpRows token rows; each lane adds
+// its 8 columns' dg sums (summed over the warp's four row groups first) once.
+// Differential attention (nsl = 5): the qd / kd gradients in dq3 come from the second softmax
+// stream run on +dO, so they enter negated, and the v gradient is dq3's minus dv2 (that
+// stream's dV).  Grid (ceil(nsl H / 8), ceil(T / kHpRows)).
 __global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
                                                             const float* __restrict__ qkv, int T, int D, int H,
-                                                            const float* __restrict__ rq, const float* __restrict__ rk,
+                                                            int nsl, const float* __restrict__ rq,
+                                                            const float* __restrict__ rk, const float* __restrict__ rq2,
+                                                            const float* __restrict__ rk2, const float* __restrict__ dv2,
                                                             const float* __restrict__ gq, const float* __restrict__ gk,
                                                             int tps, int rot, const float2* __restrict__ tab,
                                                             const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
@@ -284,13 +291,16 @@ __global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restr
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
   const int hs = blockIdx.x * 8 + warp;
-  if (hs >= 3 * H) return;
+  if (hs >= nsl * H) return;
   const int slice = hs / H, h = hs % H;
-  const int ncols = 3 * D, col = slice * D + h * 64 + 8 * j;
-  const bool norm = slice < 2;
-  const float* rs = slice == 0 ? rq : rk;
+  const int ncols = nsl * D, col = slice * D + h * 64 + 8 * j;
+  const bool norm = slice != 2;
+  const bool qside = slice == 0 || slice == 3;
+  const float* rs = slice == 0 ? rq : slice == 1 ? rk : slice == 3 ? rq2 : rk2;
+  const float sgn = slice >= 3 ? -1.f : 1.f;
+  const bool sub_dv2 = slice == 2 && dv2 != nullptr;
   float gm[8], gd[8], acc[8];
-  if (norm) ld8((slice == 0 ? gq : gk) + 8 * j, gm);
+  if (norm) ld8((qside ? gq : gk) + 8 * j, gm);
   if (g) ld8(g + col, gd);
 #pragma unroll
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
@@ -303,6 +313,16 @@ __global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restr
     float r = 0.f;
     if (valid) {
       ld8(dq3 + (long)t * ncols + col, gv);
+      if (sub_dv2) {
+        float w[8];
+        ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] -= w[k];
+      }
+      if (sgn < 0.f) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] = -gv[k];
+      }
       if (norm || g) ld8(qkv + (long)t * ncols + col, yv);
       if (norm) r = rs[(long)t * H + h];
     } else {
@@ -375,6 +395,24 @@ __global__ void add_kernel(const float* __restrict__ x, const float* __restrict_
 }
 
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
+
+// out = x - y for bf16 vectors, 8 values per thread (difference taken in f32)
+__global__ void sub_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, long n8,
+                                __nv_bfloat16* __restrict__ out) {
+  pdl_prologue();
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
+    const uint4 a = reinterpret_cast<const uint4*>(x)[i], b = reinterpret_cast<const uint4*>(y)[i];
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[k]));
+      const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[k]));
+      o[k] = pack_bf16x2(fa.x - fb.x, fa.y - fb.y);
+    }
+    reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
 
 // SwiGLU over rows: f[t] = [val (I) | gate (I)], a[t] = val * silu(gate).  Grid (I / 4 / 256
 // column blocks, T rows): each thread owns 4 consecutive columns of one row (128-bit accesses).
@@ -541,27 +579,29 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   return check_launch("head_prep_fwd", err);
 }
 
-int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, const float* rq, const float* rk,
-                 const float* gq, const float* gk, int tps, int rot, float rope_base, const float* g, __nv_bfloat16* dz,
-                 float* dg, std::string& err) {
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, int nsl, const float* rq,
+                 const float* rk, const float* rq2, const float* rk2, const float* dv2, const float* gq, const float* gk,
+                 int tps, int rot, float rope_base, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
+  if (nsl != 3 && nsl != 5) { err = "qkv backward: 3 or 5 slices"; return 1; }
   const float2* tab = nullptr;
   if (rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "qkv backward: too many rows"; return 1; }
-  if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 3 * D, c->stream) != cudaSuccess) return check_launch("memset", err);
+  if (g && cudaMemsetAsync(dg, 0, sizeof(float) * nsl * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "qkv_bwd_dz");
-  launch_pdl(c, qkv_bwd_dz_kernel, dim3((unsigned)((3 * H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows)), 256, 0,
-             dq3, qkv, T, D, H, rq, rk, gq, gk, tps, rot, tab, g, dz, dg);
+  launch_pdl(c, qkv_bwd_dz_kernel, dim3((unsigned)((nsl * H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows)), 256,
+             0, dq3, qkv, T, D, H, nsl, rq, rk, rq2, rk2, dv2, gq, gk, tps, rot, tab, g, dz, dg);
   return check_launch("qkv_bwd_dz", err);
 }
 
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
-                    int tps, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf, std::string& err) {
+                    int tps, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf, std::string& err,
+                    float gscale) {
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
-  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, dy, dy_bf);
+  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, gscale, dy, dy_bf);
   return check_launch("head_prep_bwd", err);
 }
 
@@ -579,6 +619,13 @@ int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gstride, int T, 
   if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
   launch_pdl(c, gate_bwd_kernel, dim3((unsigned)((D / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, gx, gate, gstride, T, D, tps, dy);
   return check_launch("gate_bwd", err);
+}
+
+int k_sub_bf16(Ctx* c, const __nv_bfloat16* x, const __nv_bfloat16* y, long n, __nv_bfloat16* out, std::string& err) {
+  if (n % 8) { err = "sub: n must be a multiple of 8"; return 1; }
+  ProfScope prof_(c, "sub_bf16");
+  launch_pdl(c, sub_bf16_kernel, gs(n / 8), 256, 0, x, y, n / 8, out);
+  return check_launch("sub_bf16", err);
 }
 
 int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err) {

@@ -351,6 +351,8 @@ class Dit:
     def set_tensor(self, name, qtype, host, ne0, ne1=1):
         import numpy as np
         a = np.ascontiguousarray(host)
+        if qtype == "f32" and a.nbytes < 4 * ne0 * max(ne1, 1):
+            raise Sa3kError(f"{name}: host buffer holds {a.nbytes} bytes, [{ne1}][{ne0}] f32 needs more")
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_dit_set_tensor(self._h, name.encode(), TYPE_IDS[qtype], a.ctypes.data_as(ctypes.c_void_p),
                                          ne0, ne1, err, 512), err)

@@ -4,7 +4,9 @@ through the oracle's restatement of dit_head / dit_block / dit_tail and the MSE 
 A small DiT (dim 256, 2 blocks, 4 heads, 64 memory tokens' worth of layout at reduced size) with
 Q8_0 base weights and DoRA-rows adapters on self.qkv / self.out / ff.proj / ff.out; both samples
 of the batch run in one pass.  Checked: per-sample loss, every adapter gradient (dA, dB, dm) and
-the parameters after one clipped AdamW update."""
+the parameters after one clipped AdamW update; with standard and with differential attention
+(src/dit.h:151-158, 214-240: qkv = [q | k | v | qd | kd], cross q = [cq | cqd], cross kv =
+[ck | ckd | cv], each attention output the difference of two softmax streams)."""
 import math
 
 import numpy as np
@@ -26,12 +28,12 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def _build(ctx, seed=0):
+def _build(ctx, cfg, seed=0):
     import sa3k
     import dit_synth
     rng = np.random.default_rng(seed)
-    shapes = dit_synth.tensor_shapes(CFG)
-    dit = sa3k.Dit(ctx, CFG)
+    shapes = dit_synth.tensor_shapes(cfg)
+    dit = sa3k.Dit(ctx, cfg)
     deq = {}
     for name, shape in shapes.items():
         if dit_synth.is_weight(name):
@@ -44,7 +46,7 @@ def _build(ctx, seed=0):
             v = dit_synth.synth_tensor(name, shape, rng, 0.0)
             dit.set_tensor(name, "f32", v, shape[-1], shape[0] if len(shape) > 1 else 1)
             deq[name] = v
-    targets = dit_synth.default_targets(CFG)
+    targets = dit_synth.default_targets(cfg)
     dit.init_adapters("dora-rows", RANK, ALPHA, targets)
     # adapter values: A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.05), m = row norm * U(0.9, 1.1)
     flat = np.zeros(dit.size(), np.float32)
@@ -76,11 +78,12 @@ def _inputs(rng):
     return x_t, target, tfeat, cross, glob
 
 
-def _reference(deq, ad, inputs):
+def _reference(cfg, deq, ad, inputs):
     import torch
     x_t, target, tfeat, cross, glob = inputs
-    c = oracle.DitCfg(io=CFG["io"], dim=CFG["dim"], depth=CFG["depth"], heads=CFG["heads"], cond_dim=CFG["cond_dim"],
-                      mem_tokens=CFG["mem_tokens"], rot=CFG["rot"], time_dim=CFG["time_dim"], ff_inner=CFG["ff_inner"])
+    c = oracle.DitCfg(io=cfg["io"], dim=cfg["dim"], depth=cfg["depth"], heads=cfg["heads"], cond_dim=cfg["cond_dim"],
+                      mem_tokens=cfg["mem_tokens"], rot=cfg["rot"], time_dim=cfg["time_dim"], ff_inner=cfg["ff_inner"],
+                      differential=bool(cfg["differential"]))
     T64 = lambda a: torch.tensor(np.asarray(a, np.float64))
     Wd = {k: T64(v) for k, v in deq.items()}
     lora, leaves = {}, {}
@@ -96,15 +99,16 @@ def _reference(deq, ad, inputs):
     return np.array([float(l) for l in losses]), grads
 
 
-def test_dit_step_matches_oracle(ctx):
-    import torch
-    dit, deq, ad, targets, rng = _build(ctx)
+@pytest.mark.parametrize("differential", [0, 1])
+def test_dit_step_matches_oracle(ctx, differential):
+    cfg = dict(CFG, differential=differential)
+    dit, deq, ad, targets, rng = _build(ctx, cfg)
     # the device initialises m to the dequantized base row norms (train_row_norms)
     for name in targets:
         _, nrm = oracle.row_norms(deq[name])
         np.testing.assert_allclose(ad[name]["m_dev"], nrm, rtol=1e-6)
     inputs = _inputs(rng)
-    ref_loss, ref_grads = _reference(deq, ad, inputs)
+    ref_loss, ref_grads = _reference(cfg, deq, ad, inputs)
 
     dit.zero_grads()
     loss = np.zeros(B, np.float32)
@@ -138,3 +142,26 @@ def test_dit_step_matches_oracle(ctx):
     oracle.adamw_f32(rp, g, np.zeros_like(rp), np.zeros_like(rp), 1e-3, 0.9, 0.999, 1e-8, 0.01, 1)
     assert abs(norm - ref_norm) <= 1e-6 * ref_norm
     np.testing.assert_allclose(p1, rp, rtol=1e-6, atol=1e-8)
+
+
+def test_dit_rejects_misshaped_tensors(ctx):
+    """Every tensor is checked against the config's shape on upload (a differential config wants
+    a 5 dim qkv projection, 2 dim cross q and 3 dim cross kv); unknown names are refused."""
+    import sa3k
+    for diff in (0, 1):
+        dit = sa3k.Dit(ctx, dict(CFG, differential=diff))
+        D = CFG["dim"]
+        bad_rows = (3 if diff else 5) * D
+        w = np.zeros((bad_rows, D), np.float32)
+        with pytest.raises(sa3k.Sa3kError, match="expected"):
+            dit.set_tensor("dit.0.self.qkv.weight", "q8_0", oracle.quantize(w, "q8_0"), D, bad_rows)
+        kv_rows = (2 if diff else 3) * D
+        with pytest.raises(sa3k.Sa3kError, match="expected"):
+            dit.set_tensor("dit.1.cross.kv.weight", "f32", np.zeros((kv_rows, D), np.float32), D, kv_rows)
+        with pytest.raises(sa3k.Sa3kError, match="not a tensor"):
+            dit.set_tensor("dit.2.ssg", "f32", np.zeros(6 * D, np.float32), 6 * D, 1)   # depth is 2
+        with pytest.raises(sa3k.Sa3kError, match="not a tensor"):
+            dit.set_tensor("vae.encoder.weight", "f32", np.zeros((D, D), np.float32), D, D)
+        ok = (5 if diff else 3) * D
+        dit.set_tensor("dit.0.self.qkv.weight", "f32", np.zeros((ok, D), np.float32), D, ok)
+        dit.close()
