@@ -267,8 +267,10 @@ void sa3k_dit_free(sa3k_dit* dit);
 int sa3k_dit_set_tensor(sa3k_dit* dit, const char* name, int ggml_type, const void* host,
                         int64_t ne0, int64_t ne1, char* err, int err_len);
 
-/* Functional adapters ("lora" or "dora-rows", rank <= 16) on the named per-block weights.
- * Allocates the flat adapter state [A | B | m] per target (order of `names`), zero; for
+/* Functional adapters ("lora" or "dora-rows", rank <= 16) on the named weights: any 2-D
+ * "*.weight" of the DiT, so the reference's `full` and `core` target scopes
+ * (enumerate_train_lora_targets, src/train_lora.h:54-117) both fit; head adapters get their
+ * gradient through x0, the context and gcond.  Allocates the flat adapter state [A | B | m] per target (order of `names`), zero; for
  * dora-rows computes base_norm_sq and initialises m to the base row norms (src/train_lora.h:
  * 141-174, 262-263).  A and B are then written by the caller through sa3k_dit_adapter_buffer.
  * Counterpart of init_train_lora_state (src/train_lora.h:205-273) for the device state. */

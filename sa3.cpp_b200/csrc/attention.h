@@ -59,7 +59,8 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
 // forward input y and the saved rstd.
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& s,
                     int tokens_per_sample, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf,
-                    std::string& err, float gscale = 1.0f);   // g enters multiplied by gscale
+                    std::string& err, float gscale = 1.0f,     // g enters as gscale (g - g2)
+                    const float* g2 = nullptr, long g2_ld = 0);
 // Self-attention q/k/v head preparation backward (dq3 = [dq | dk | dv] f32, or with nsl = 5 the
 // differential layout [dq | dk | dv | dqd | dkd] whose second stream ran on +dO, dv2 its dV, and
 // rq2 / rk2 its rstd; qkv = the projection output) fused with the qkv projection's backward
@@ -90,6 +91,16 @@ int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string&
 
 // mod[b][i] = ssg[i] + gcond[b][i] for i < 6*D, and the two gates sigmoid(1 - g) in place of
 // slots 2 and 5 (the adaLN-zero vectors of src/dit.h:174-193)
+// out = dy * silu'(h) (elementwise; out may alias dy)
+int k_silu_bwd(Ctx* c, const float* dy, const float* h, long n, float* out, std::string& err);
+// adaLN modulation gradient, added per sample into [B][out_stride] rows (rows t of sample t / tps):
+// of h = rms_norm(x) (1 + sc) + sh:  dsc += gamma * colsum(dh * x * rstd), dsh += colsum(dh);
+// of out = res + y * s, s = sigmoid(1 - g) (gate holds s, as the modulation kernel leaves it):
+// dg += -s (1 - s) colsum(gy * y)
+int k_mod_grad_norm(Ctx* c, const float* dh, const float* x, const float* rstd, const float* gamma, int T, int D,
+                    int tps, long out_stride, float* dsc, float* dsh, std::string& err);
+int k_mod_grad_gate(Ctx* c, const float* gy, const float* y, const float* gate, long gate_stride, int T, int D, int tps,
+                    long out_stride, float* dgate, std::string& err);
 int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err);
 
 // loss[b] = sum((vel - target)^2) / (io*T) per sample; dvel = 2 (vel - target) / (io*T)

