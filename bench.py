@@ -583,6 +583,8 @@ def main_dit(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     cfg = dit_cfg()
+    if args.depth:
+        cfg["depth"] = args.depth   # profiling of per-block kernels on a shallower stack only
     B, T, C = DIT_B, DIT_T, DIT_CTX
     ctx = sa3k.Context(local)
     dit = build_dit(ctx, cfg, seed=1234)                 # identical base + adapters on every rank
@@ -717,7 +719,8 @@ def main_dit(args):
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": DIT_WORKLOAD, "global_batch": B * world, "seq_len": T,
+            "config": {"workload": DIT_WORKLOAD + (f" (depth overridden to {cfg['depth']})" if args.depth else ""),
+                       "global_batch": B * world, "seq_len": T,
                        "parallelism": f"dp{world}", "l2": "256 MB flush between timed steps"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": None,
@@ -846,6 +849,9 @@ def main():
     ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
     ap.add_argument("--workload", default="dit", choices=["dit", "linear", "attention"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--depth", type=int, default=0,
+                    help="dit: override the block count (small device footprint for ncu captures of per-block "
+                         "kernels; the benchmark line is quoted at the configured 24)")
     ap.add_argument("--profile-step", action="store_true",
                     help="dit: bracket one extra graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()

@@ -39,6 +39,10 @@ int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, 
                       std::string& err);
 // gx += d/dx of the above for upstream dh (gamma, sc, sh are frozen); gx_bf (nullable) also
 // receives the updated gx as bf16
+// x_out = x_in + y * gate[sample] (gate null: x_in + y), then the rmsnorm_mod_fwd of x_out
+int k_residual_norm(Ctx* c, const float* x_in, const float* y, const float* gate, long gstride, int T, int D, int tps,
+                    float* x_out, const float* gamma, const float* sc, const float* sh, long mod_stride, float eps,
+                    __nv_bfloat16* h, float* rstd, std::string& err);
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
                       const float* sc, long mod_stride, int tokens_per_sample, float* gx, __nv_bfloat16* gx_bf,
                       std::string& err);

@@ -741,30 +741,41 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         if (!waitw(&s_full[t % 3], (uint32_t)((t / 3) & 1), kErrTimeoutAccum)) { ok = false; continue; }
         tc_fence_after();
         const uint32_t tS = tbase + 128 * (t % 3);
-        uint32_t sv[64], pv[64];
-        tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
-        tmem_ld32(tS + 64 + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
-        tmem_ld_wait();
         const int k0 = (c.t0 + j) * 64;
-        if (!tile_visible(q0, 128, k0, 64, a.Sk, a.window)) {
-#pragma unroll
-          for (int cc = 0; cc < 64; ++cc)
-            if (!visible(qi, k0 + cc, a.Sk, a.window)) sv[cc] = __float_as_uint(-INFINITY);
-        }
+        const bool edge = !tile_visible(q0, 128, k0, 64, a.Sk, a.window);
         const uint64_t sc2 = f2(a.sl2, a.sl2), nl2 = f2(-lse, -lse), nd2 = f2(-Dq, -Dq);
-        uint32_t pk[32];   // dS row as packed bf16 pairs: column e holds keys 2e, 2e + 1
+        // two halves of 32 keys: S / dP of a half in, its dS row (packed bf16 pairs, column e of
+        // the slot holds keys 2e, 2e + 1) out to the half's 16 columns, which the other half no
+        // longer reads
+#pragma unroll 1
+        for (int hf = 0; hf < 2; ++hf) {
+          uint32_t sv[32], pv[32];
+          tmem_ld32(tS + lane_off + 32 * hf, sv);
+          tmem_ld32(tS + 64 + lane_off + 32 * hf, pv);
+          tmem_ld_wait();
+          if (edge) {
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float x0, x1, d0, d1;
-          f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
-          const uint64_t pp = f2(ex2(x0), ex2(x1));
-          f2split(fmul2(pp, fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0, d1);
-          pk[e] = pack_bf16x2(d0, d1);
+            for (int cc = 0; cc < 32; ++cc)
+              if (!visible(qi, k0 + 32 * hf + cc, a.Sk, a.window)) sv[cc] = __float_as_uint(-INFINITY);
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float x0, x1, d0, d1;
+            f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
+            float p0, p1;
+            if (kPolyPair[e & 7]) {      // a share of the exponentials on the FMA pipes
+              ex2_poly2(x0, x1, p0, p1);
+            } else {
+              p0 = ex2(x0);
+              p1 = ex2(x1);
+            }
+            const uint64_t pp = f2(p0, p1);
+            f2split(fmul2(pp, fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0, d1);
+            pk[e] = pack_bf16x2(d0, d1);
+          }
+          tmem_st16(tS + lane_off + 16 * hf, pk);
         }
-        tmem_st16(tS + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-        tmem_st16(tS + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -958,37 +969,47 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       if (!ok) continue;
       tc_fence_after();
       const uint32_t tS = tbase + 128 * (i % 3);
-      uint32_t sv[64], pv[64];
-      tmem_ld32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld32(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
-      tmem_ld32(tS + 64 + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
-      tmem_ld_wait();
-      if (!tile_visible(k0, 128, q0, 64, a.Sq, a.window) || kj >= a.Sk) {
-        // (queries past Sq already carry lse = +inf, so P = 0 there)
-#pragma unroll
-        for (int c = 0; c < 64; ++c)
-          if (!visible(q0 + c, kj, a.Sk, a.window)) sv[c] = __float_as_uint(-INFINITY);
-      }
+      const bool edge = !tile_visible(k0, 128, q0, 64, a.Sq, a.window) || kj >= a.Sk;
       const uint64_t sc2 = f2(a.sl2, a.sl2);
       const float2* lse2 = reinterpret_cast<const float2*>(lse_b);
       const float2* D2 = reinterpret_cast<const float2*>(D_b);
-      uint32_t pk[32], dk[32];
+      // two halves of 32 queries: S^T / dP^T of a half in, its P^T / dS^T (packed bf16) out to the
+      // first 16 columns of the half's slot (the packed halves never overlap columns still to read),
+      // so about 100 values per thread are live instead of 192
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t sv[32], pv[32];
+        tmem_ld32(tS + lane_off + 32 * hf, sv);
+        tmem_ld32(tS + 64 + lane_off + 32 * hf, pv);
+        tmem_ld_wait();
+        if (edge) {
+          // (queries past Sq already carry lse = +inf, so P = 0 there)
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float2 lz = lse2[e], dz = D2[e];      // smem broadcast reads
-        float x0, x1, d0, d1;
-        f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, f2(-lz.x, -lz.y)), x0, x1);
-        const float p0 = ex2(x0), p1 = ex2(x1);
-        f2split(fmul2(f2(p0, p1), fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])),
-                                        f2(-dz.x, -dz.y))), d0, d1);
-        pk[e] = pack_bf16x2(p0, p1);
-        dk[e] = pack_bf16x2(d0, d1);
+          for (int c = 0; c < 32; ++c)
+            if (!visible(q0 + 32 * hf + c, kj, a.Sk, a.window)) sv[c] = __float_as_uint(-INFINITY);
+        }
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float2 lz = lse2[16 * hf + e], dz = D2[16 * hf + e];      // smem broadcast reads
+          float x0, x1, d0, d1;
+          f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, f2(-lz.x, -lz.y)), x0,
+                  x1);
+          float p0, p1;
+          if (kPolyPair[e & 7]) {      // a share of the exponentials on the FMA pipes
+            ex2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          f2split(fmul2(f2(p0, p1), fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])),
+                                          f2(-dz.x, -dz.y))), d0, d1);
+          pk[e] = pack_bf16x2(p0, p1);
+          dk[e] = pack_bf16x2(d0, d1);
+        }
+        tmem_st16(tS + lane_off + 16 * hf, pk);
+        tmem_st16(tS + 64 + lane_off + 16 * hf, dk);
       }
-      tmem_st16(tS + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&pk[0]));
-      tmem_st16(tS + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&pk[16]));
-      tmem_st16(tS + 64 + lane_off, *reinterpret_cast<uint32_t(*)[16]>(&dk[0]));
-      tmem_st16(tS + 64 + lane_off + 16, *reinterpret_cast<uint32_t(*)[16]>(&dk[16]));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();

@@ -533,6 +533,13 @@ static int dit_step(DitModel& m, std::string& err) {
   }
 
   // ---------------- blocks (src/dit.h:164-266)
+  // every block's adaLN vectors first: the residual kernel ending block l also forms the
+  // modulated pre-norm input of block l + 1
+  for (int l = 0; l < k.depth; ++l) {
+    const float* ssg = m.vec(m.bname(l, "ssg"), err);
+    if (!ssg) return 1;
+    if (k_modulation(c, ssg, m.gcond, B, D, m.blk[l].mod, err)) return 1;
+  }
   for (int l = 0; l < k.depth; ++l) {
     DitBlockAct& a = m.blk[l];
     float* x_next = l + 1 < k.depth ? m.blk[l + 1].x : m.x_final;
@@ -553,9 +560,11 @@ static int dit_step(DitModel& m, std::string& err) {
     DitTarget *tcq = target(m, m.bname(l, "cross.q.weight")), *tkv = target(m, m.bname(l, "cross.kv.weight"));
     DitTarget* tco = target(m, m.bname(l, "cross.out.weight"));
     const long ms = 6L * D;
-    if (k_modulation(c, ssg, m.gcond, B, D, a.mod, err)) return 1;
-    // self-attention branch
-    if (k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err)) return 1;
+    // self-attention branch (block 0's pre-norm here; every later one ran fused with the residual
+    // step that ended the previous block)
+    if (l == 0 &&
+        k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err))
+      return 1;
     if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, err)) return 1;
     {
       // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE
@@ -577,9 +586,10 @@ static int dit_step(DitModel& m, std::string& err) {
       if (k_sub_bf16(c, a.o1, a.o2, M * D, a.oa, err)) return 1;
     }
     if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, err)) return 1;
-    if (k_gate_residual(c, a.x, a.yo, a.mod + 2 * D, ms, (int)M, D, S, a.x1, err)) return 1;
-    // cross-attention branch
-    if (k_rmsnorm_mod_fwd(c, a.x1, (int)M, D, g_cn, nullptr, nullptr, 0, S, k.norm_eps, a.hc, a.rstd_c, err)) return 1;
+    // x1 = x + gate(yo), then the cross-attention branch's norm of x1
+    if (k_residual_norm(c, a.x, a.yo, a.mod + 2 * D, ms, (int)M, D, S, a.x1, g_cn, nullptr, nullptr, 0, k.norm_eps,
+                        a.hc, a.rstd_c, err))
+      return 1;
     if (lin_fwd(m, wcq, tcq, nullptr, a.hc, M, a.qf, nullptr, err)) return 1;
     {
       // [cq (| cqd)], both with cross.q_norm, no RoPE
@@ -607,14 +617,24 @@ static int dit_step(DitModel& m, std::string& err) {
       if (k_sub_bf16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
     }
     if (lin_fwd(m, wco, tco, nullptr, a.oc, M, tco ? a.yc : m.dtmp, nullptr, err)) return 1;
-    if (k_add(c, a.x1, tco ? a.yc : m.dtmp, (long)M * D, a.x2, err)) return 1;
-    // feed-forward branch
-    if (k_rmsnorm_mod_fwd(c, a.x2, (int)M, D, g_ff, a.mod + 3 * D, a.mod + 4 * D, ms, S, k.norm_eps, a.hf, a.rstd_f, err))
+    // x2 = x1 + cross-attention output, then the feed-forward branch's modulated norm of x2
+    if (k_residual_norm(c, a.x1, tco ? a.yc : m.dtmp, nullptr, 0, (int)M, D, S, a.x2, g_ff, a.mod + 3 * D,
+                        a.mod + 4 * D, ms, k.norm_eps, a.hf, a.rstd_f, err))
       return 1;
     if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, a.ff, nullptr, err)) return 1;
     if (k_swiglu_fwd(c, a.ff, (int)M, I, a.act, err)) return 1;
     if (lin_fwd(m, wfo, tf, b_fo, a.act, M, a.yf, nullptr, err)) return 1;
-    if (k_gate_residual(c, a.x2, a.yf, a.mod + 5 * D, ms, (int)M, D, S, x_next, err)) return 1;
+    if (l + 1 < k.depth) {
+      // x_next = x2 + gate(yf), then block l + 1's modulated pre-norm of it
+      DitBlockAct& an = m.blk[l + 1];
+      const float* g_pre_n = m.vec(m.bname(l + 1, "pre_norm.gamma"), err);
+      if (!g_pre_n) return 1;
+      if (k_residual_norm(c, a.x2, a.yf, a.mod + 5 * D, ms, (int)M, D, S, x_next, g_pre_n, an.mod, an.mod + D, ms,
+                          k.norm_eps, an.h_a, an.rstd_a, err))
+        return 1;
+    } else if (k_gate_residual(c, a.x2, a.yf, a.mod + 5 * D, ms, (int)M, D, S, x_next, err)) {
+      return 1;
+    }
   }
 
   // ---------------- tail + loss (src/dit.h:314-323, src/train_ckpt.h:223-228)

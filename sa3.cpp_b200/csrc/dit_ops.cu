@@ -15,87 +15,6 @@
 namespace sa3k {
 namespace {
 
-__global__ void rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D, const float* __restrict__ gamma,
-                                       const float* __restrict__ sc, const float* __restrict__ sh, long mod_stride,
-                                       int tps, float eps, __nv_bfloat16* __restrict__ h, float* __restrict__ rstd) {
-  pdl_prologue();
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= T) return;
-  const int lane = threadIdx.x & 31;
-  const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
-  float ss = 0.f;
-  for (int i = lane; i < D / 4; i += 32) {
-    const float4 v = xr[i];
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)D + eps);
-  if (lane == 0 && rstd) rstd[row] = r;
-  const int s = row / tps;
-  const float* scs = sc ? sc + (long)s * mod_stride : nullptr;
-  const float* shs = sh ? sh + (long)s * mod_stride : nullptr;
-  uint2* hr = reinterpret_cast<uint2*>(h + (long)row * D);
-  for (int i = lane; i < D / 4; i += 32) {
-    const float4 v = xr[i];
-    const float4 gm = reinterpret_cast<const float4*>(gamma)[i];
-    float o[4] = {v.x * r * gm.x, v.y * r * gm.y, v.z * r * gm.z, v.w * r * gm.w};
-    if (scs) {
-      const float4 a = reinterpret_cast<const float4*>(scs)[i];
-      const float4 b = reinterpret_cast<const float4*>(shs)[i];
-      o[0] = o[0] * (1.f + a.x) + b.x;
-      o[1] = o[1] * (1.f + a.y) + b.y;
-      o[2] = o[2] * (1.f + a.z) + b.z;
-      o[3] = o[3] * (1.f + a.w) + b.w;
-    }
-    uint2 pk;
-    pk.x = pack_bf16x2(o[0], o[1]);
-    pk.y = pack_bf16x2(o[2], o[3]);
-    hr[i] = pk;
-  }
-}
-
-__global__ void rmsnorm_mod_bwd_kernel(const float* __restrict__ dh, const float* __restrict__ x,
-                                       const float* __restrict__ rstd, int T, int D, const float* __restrict__ gamma,
-                                       const float* __restrict__ sc, long mod_stride, int tps, float* __restrict__ gx,
-                                       __nv_bfloat16* __restrict__ gx_bf) {
-  pdl_prologue();
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= T) return;
-  const int lane = threadIdx.x & 31;
-  const float r = rstd[row];
-  const int s = row / tps;
-  const float* scs = sc ? sc + (long)s * mod_stride : nullptr;
-  const float4* xr = reinterpret_cast<const float4*>(x + (long)row * D);
-  const float4* dr = reinterpret_cast<const float4*>(dh + (long)row * D);
-  float dot = 0.f;
-  for (int i = lane; i < D / 4; i += 32) {
-    const float4 v = xr[i], d = dr[i], gm = reinterpret_cast<const float4*>(gamma)[i];
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (scs) a = reinterpret_cast<const float4*>(scs)[i];
-    dot += d.x * gm.x * (1.f + a.x) * v.x + d.y * gm.y * (1.f + a.y) * v.y + d.z * gm.z * (1.f + a.z) * v.z +
-           d.w * gm.w * (1.f + a.w) * v.w;
-  }
-  dot = warp_sum(dot) * r / (float)D;   // mean(dn * n)
-  float4* gr = reinterpret_cast<float4*>(gx + (long)row * D);
-  for (int i = lane; i < D / 4; i += 32) {
-    const float4 v = xr[i], d = dr[i], gm = reinterpret_cast<const float4*>(gamma)[i];
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (scs) a = reinterpret_cast<const float4*>(scs)[i];
-    float4 gv = gr[i];
-    gv.x += r * (d.x * gm.x * (1.f + a.x) - v.x * r * dot);
-    gv.y += r * (d.y * gm.y * (1.f + a.y) - v.y * r * dot);
-    gv.z += r * (d.z * gm.z * (1.f + a.z) - v.z * r * dot);
-    gv.w += r * (d.w * gm.w * (1.f + a.w) - v.w * r * dot);
-    gr[i] = gv;
-    if (gx_bf) {
-      uint2 pk;
-      pk.x = pack_bf16x2(gv.x, gv.y);
-      pk.y = pack_bf16x2(gv.z, gv.w);
-      reinterpret_cast<uint2*>(gx_bf + (long)row * D)[i] = pk;
-    }
-  }
-}
-
 // RoPE angle of pair i (< rot/2) at position pos: pos * base^(-2i/rot); its (cos, sin) come from
 // a table built once per (positions, rot, base) rather than from sincos in every warp.
 __global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __restrict__ tab) {
@@ -118,7 +37,8 @@ struct HeadSlices {
   HeadSlice s[5];
   int n;
 };
-constexpr int kHpRows = 32;
+constexpr int kHpRows = 16;
+constexpr int kQkvRows = 32;   // qkv_bwd_dz: more rows per block, fewer dg atomics
 
 __device__ __forceinline__ float sum8(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -144,6 +64,146 @@ __device__ __forceinline__ void st8_bf16(__nv_bfloat16* p, const float (&v)[8]) 
   o.z = pack_bf16x2(v[4], v[5]);
   o.w = pack_bf16x2(v[6], v[7]);
   *reinterpret_cast<uint4*>(p) = o;
+}
+
+// Sum over the block (blockDim.x a multiple of 32, at most 1024); every thread gets the total.
+// `red` holds 32 floats of shared memory, used once per kernel.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  return warp_sum(l < nw ? red[l] : 0.f);
+}
+
+// rms_norm + adaLN modulate of one row per block, one thread per 8 columns: every load of the row
+// (x, gamma, the sample's scale / shift) is issued before the row reduction, so the whole row is
+// in flight at once.  h = bf16(x rstd gamma (1 + sc) + sh), rstd = 1 / sqrt(mean(x^2) + eps).
+__global__ void __launch_bounds__(1024) rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D,
+                                                               const float* __restrict__ gamma,
+                                                               const float* __restrict__ sc,
+                                                               const float* __restrict__ sh, long mod_stride, int tps,
+                                                               float eps, __nv_bfloat16* __restrict__ h,
+                                                               float* __restrict__ rstd) {
+  pdl_prologue();
+  __shared__ float red[32];
+  const int row = blockIdx.x, c = 8 * threadIdx.x;
+  const bool act = c < D;
+  const long s = row / tps;
+  float v[8], gm[8], a[8], b[8];
+  if (act) {
+    ld8(x + (long)row * D + c, v);
+    ld8(gamma + c, gm);
+    if (sc) {
+      ld8(sc + s * mod_stride + c, a);
+      ld8(sh + s * mod_stride + c, b);
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = 0.f;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+  const float r = rsqrtf(block_sum(ss, red) / (float)D + eps);
+  if (threadIdx.x == 0 && rstd) rstd[row] = r;
+  if (!act) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[k] *= r * gm[k];
+    if (sc) v[k] = fmaf(v[k], 1.f + a[k], b[k]);
+  }
+  st8_bf16(h + (long)row * D + c, v);
+}
+
+// The residual step of a block half fused with the norm that follows it, one row per block, one
+// thread per 8 columns: x_out = x_in + y (gate null: the cross-attention residual) or
+// x_in + y s (s = the sample's gate vector, sigmoid(1 - g) as the modulation kernel leaves it),
+// then h = bf16(rms_norm(x_out) gamma (1 + sc) + sh) and its rstd, as rmsnorm_mod_fwd.
+__global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __restrict__ x_in,
+                                                             const float* __restrict__ y,
+                                                             const float* __restrict__ gate, long gstride, int T,
+                                                             int D, int tps, float* __restrict__ x_out,
+                                                             const float* __restrict__ gamma,
+                                                             const float* __restrict__ sc,
+                                                             const float* __restrict__ sh, long mod_stride, float eps,
+                                                             __nv_bfloat16* __restrict__ h, float* __restrict__ rstd) {
+  pdl_prologue();
+  __shared__ float red[32];
+  const int row = blockIdx.x, c = 8 * threadIdx.x;
+  const bool act = c < D;
+  const long s = row / tps;
+  const long e = (long)row * D + c;
+  float v[8], w[8], gv[8], gm[8], a[8], b[8];
+  if (act) {
+    ld8(x_in + e, v);
+    ld8(y + e, w);
+    if (gate) ld8(gate + s * gstride + c, gv);
+    ld8(gamma + c, gm);
+    if (sc) {
+      ld8(sc + s * mod_stride + c, a);
+      ld8(sh + s * mod_stride + c, b);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = gate ? fmaf(w[k], gv[k], v[k]) : v[k] + w[k];
+    st8(x_out + e, v);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = 0.f;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) ss = fmaf(v[k], v[k], ss);
+  const float r = rsqrtf(block_sum(ss, red) / (float)D + eps);
+  if (threadIdx.x == 0 && rstd) rstd[row] = r;
+  if (!act) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[k] *= r * gm[k];
+    if (sc) v[k] = fmaf(v[k], 1.f + a[k], b[k]);
+  }
+  st8_bf16(h + e, v);
+}
+
+// Backward of rmsnorm_mod_fwd, one row per block (as the forward): with dn = dh gamma (1 + sc),
+// gx += rstd (dn - x rstd^2 mean(dn x)); gx_bf (nullable) receives bf16(gx) as well.
+__global__ void __launch_bounds__(1024) rmsnorm_mod_bwd_kernel(const float* __restrict__ dh,
+                                                               const float* __restrict__ x,
+                                                               const float* __restrict__ rstd, int T, int D,
+                                                               const float* __restrict__ gamma,
+                                                               const float* __restrict__ sc, long mod_stride, int tps,
+                                                               float* __restrict__ gx,
+                                                               __nv_bfloat16* __restrict__ gx_bf) {
+  pdl_prologue();
+  __shared__ float red[32];
+  const int row = blockIdx.x, c = 8 * threadIdx.x;
+  const bool act = c < D;
+  const long s = row / tps;
+  const long e = (long)row * D + c;
+  float v[8], d[8], gm[8], a[8], g[8];
+  const float r = rstd[row];
+  if (act) {
+    ld8(x + e, v);
+    ld8(dh + e, d);
+    ld8(gamma + c, gm);
+    ld8(gx + e, g);
+    if (sc) ld8(sc + s * mod_stride + c, a);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = d[k] = 0.f;
+  }
+  float dot = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    if (act) d[k] *= gm[k] * (sc ? 1.f + a[k] : 1.f);   // dn
+    dot = fmaf(d[k], v[k], dot);
+  }
+  dot = block_sum(dot, red) * r / (float)D;   // rstd mean(dn x)
+  if (!act) return;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) g[k] += r * (d[k] - v[k] * r * dot);
+  st8(gx + e, g);
+  if (gx_bf) st8_bf16(gx_bf + e, g);
 }
 
 // RoPE of this lane's chunk j at position pos (inverse rotation when inv): first element of a pair
@@ -191,16 +251,23 @@ __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const float* __restr
   }
   const int tb0 = blockIdx.y * kHpRows;
   int pos = (tb0 + q) % tps;
-#pragma unroll 2
-  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
+  // every row's load first (the rstd stores below may alias y for the compiler)
+  float vr[kHpRows / 4][8];
+#pragma unroll
+  for (int it = 0; it < kHpRows / 4; ++it) {
+    const int t = tb0 + 4 * it + q;
+    if (t < T) {
+      ld8(y + (long)t * ncols + col, vr[it]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) vr[it][k] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < kHpRows / 4; ++it) {
     const int t = tb0 + 4 * it + q;
     const bool valid = t < T;
-    float v[8];
-    if (valid) ld8(y + (long)t * ncols + col, v);
-    else {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = 0.f;
-    }
+    float (&v)[8] = vr[it];
     if (sl.gamma) {
       float ss = 0.f;
 #pragma unroll
@@ -286,7 +353,7 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
 // Differential attention (nsl = 5): the qd / kd gradients in dq3 come from the second softmax
 // stream run on +dO, so they enter negated, and the v gradient is dq3's minus dv2 (that
 // stream's dV).  Grid (ceil(nsl H / 8), ceil(T / kHpRows)).
-__global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
+__global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
                                                             const float* __restrict__ qkv, int T, int D, int H,
                                                             int nsl, const float* __restrict__ rq,
                                                             const float* __restrict__ rk, const float* __restrict__ rq2,
@@ -311,30 +378,42 @@ __global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restr
   if (g) ld8(g + col, gd);
 #pragma unroll
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-  const int tb0 = blockIdx.y * kHpRows;
+  const int tb0 = blockIdx.y * kQkvRows;
   int pos = (tb0 + q) % tps;
-  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
-    const int t = tb0 + 4 * it + q;
-    const bool valid = t < T;
-    float gv[8], yv[8];
-    float r = 0.f;
-    if (valid) {
-      ld8(dq3 + (long)t * ncols + col, gv);
-      if (sub_dv2) {
-        float w[8];
-        ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
+  // rows in pairs, both rows' loads issued before either is used (the dz stores in between may
+  // alias the inputs for the compiler)
+  float gvr[2][8], yvr[2][8], rr[2];
+#pragma unroll 1
+  for (int it0 = 0; it0 < kQkvRows / 4 && tb0 + 4 * it0 < T; it0 += 2) {
 #pragma unroll
-        for (int k = 0; k < 8; ++k) gv[k] -= w[k];
-      }
-      if (sgn < 0.f) {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) gv[k] = -gv[k];
-      }
-      if (norm || g) ld8(qkv + (long)t * ncols + col, yv);
-      if (norm) r = rs[(long)t * H + h];
+  for (int u = 0; u < 2; ++u) {
+    const int t = tb0 + 4 * (it0 + u) + q;
+    rr[u] = 0.f;
+    if (t < T) {
+      ld8(dq3 + (long)t * ncols + col, gvr[u]);
+      if (norm || g) ld8(qkv + (long)t * ncols + col, yvr[u]);
+      if (norm) rr[u] = rs[(long)t * H + h];
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] = yv[k] = 0.f;
+      for (int k = 0; k < 8; ++k) gvr[u][k] = yvr[u][k] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < 2; ++u) {
+    const int t = tb0 + 4 * (it0 + u) + q;
+    const bool valid = t < T;
+    float (&gv)[8] = gvr[u];
+    const float (&yv)[8] = yvr[u];
+    const float r = rr[u];
+    if (valid && sub_dv2) {
+      float w[8];
+      ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] -= w[k];
+    }
+    if (sgn < 0.f) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] = -gv[k];
     }
     if (norm) {
       if (rot == 32 || rot == 64) rope8(gv, j, pos, rot, tab, true);
@@ -355,6 +434,7 @@ __global__ void __launch_bounds__(256, 3) qkv_bwd_dz_kernel(const float* __restr
     if (valid) st8_bf16(dz + (long)t * ncols + col, gv);
     pos += 4;
     while (pos >= tps) pos -= tps;
+  }
   }
   if (g) {
 #pragma unroll
@@ -576,19 +656,38 @@ unsigned gs(long n, int threads = 256) {
 
 }  // namespace
 
+// one block per row, one thread per 8 columns, in whole warps
+static int row_block(int D, std::string& err) {
+  if (D % 8 || D > 8192) { err = "rms_norm: D must be a multiple of 8 and at most 8192"; return 0; }
+  return (D / 8 + 31) / 32 * 32;
+}
+
 int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, const float* sc, const float* sh,
                       long mod_stride, int tps, float eps, __nv_bfloat16* h, float* rstd, std::string& err) {
-  if (D % 4) { err = "rms_norm: D % 4"; return 1; }
+  const int nt = row_block(D, err);
+  if (!nt) return 1;
   ProfScope prof_(c, "rmsnorm_mod_fwd");
-  launch_pdl(c, rmsnorm_mod_fwd_kernel, (unsigned)((T + 7) / 8), 256, 0, x, T, D, gamma, sc, sh, mod_stride, tps, eps, h, rstd);
+  launch_pdl(c, rmsnorm_mod_fwd_kernel, (unsigned)T, nt, 0, x, T, D, gamma, sc, sh, mod_stride, tps, eps, h, rstd);
   return check_launch("rmsnorm_mod_fwd", err);
+}
+
+int k_residual_norm(Ctx* c, const float* x_in, const float* y, const float* gate, long gstride, int T, int D, int tps,
+                    float* x_out, const float* gamma, const float* sc, const float* sh, long mod_stride, float eps,
+                    __nv_bfloat16* h, float* rstd, std::string& err) {
+  const int nt = row_block(D, err);
+  if (!nt) return 1;
+  ProfScope prof_(c, "residual_norm");
+  launch_pdl(c, residual_norm_kernel, (unsigned)T, nt, 0, x_in, y, gate, gstride, T, D, tps, x_out, gamma, sc, sh,
+             mod_stride, eps, h, rstd);
+  return check_launch("residual_norm", err);
 }
 
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
                       const float* sc, long mod_stride, int tps, float* gx, __nv_bfloat16* gx_bf, std::string& err) {
+  const int nt = row_block(D, err);
+  if (!nt) return 1;
   ProfScope prof_(c, "rmsnorm_mod_bwd");
-  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)((T + 7) / 8), 256, 0, dh, x, rstd, T, D, gamma, sc, mod_stride,
-             tps, gx, gx_bf);
+  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)T, nt, 0, dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx, gx_bf);
   return check_launch("rmsnorm_mod_bwd", err);
 }
 
@@ -641,10 +740,10 @@ int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H
   if (nsl != 3 && nsl != 5) { err = "qkv backward: 3 or 5 slices"; return 1; }
   const float2* tab = nullptr;
   if (rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
-  if ((T + kHpRows - 1) / kHpRows > 65535) { err = "qkv backward: too many rows"; return 1; }
+  if ((T + kQkvRows - 1) / kQkvRows > 65535) { err = "qkv backward: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * nsl * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "qkv_bwd_dz");
-  launch_pdl(c, qkv_bwd_dz_kernel, dim3((unsigned)((nsl * H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows)), 256,
+  launch_pdl(c, qkv_bwd_dz_kernel, dim3((unsigned)((nsl * H + 7) / 8), (unsigned)((T + kQkvRows - 1) / kQkvRows)), 256,
              0, dq3, qkv, T, D, H, nsl, rq, rk, rq2, rk2, dv2, gq, gk, tps, rot, tab, g, dz, dg);
   return check_launch("qkv_bwd_dz", err);
 }

@@ -11,6 +11,8 @@
 #include "sa3k_internal.h"
 #include "lora_kernels.h"
 
+#include <algorithm>
+
 namespace sa3k {
 
 constexpr int R = 16;   // padded rank
@@ -125,6 +127,7 @@ __global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __re
 // z = (y - bias) / g the pre-scale output of the forward.  Thread = 4 columns, block = kFuseTok
 // rows (one f32 atomic per column and block).
 constexpr int kFuseTok = 32;
+constexpr int kGateRows = 16;
 
 __device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4], const float (&gv)[4], bool dora) {
   uint2 pk;
@@ -134,8 +137,8 @@ __device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4
 }
 
 // dy = gx * gate[sample] (the gate backward of src/dit.h:186-193).  Block (128, 4): thread x owns
-// 4 columns, thread y a quarter of the block's kFuseTok rows (four rows at a time, loads first);
-// dg is summed over y in shared memory before one atomic per column.
+// 4 columns, thread y four consecutive rows of each kGateRows-row chunk the block visits (loads
+// first); dg is summed over y in shared memory before one atomic per column.
 __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate,
                                                           long gstride, int T, int D, int tps,
                                                           const float* __restrict__ y, const float* __restrict__ bias,
@@ -145,8 +148,6 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
   __shared__ float4 red[4][128];
   const int c0 = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   const bool col_ok = c0 < D;
-  const int rq = kFuseTok / 4;
-  const int t0 = blockIdx.y * kFuseTok + threadIdx.y * rq, t1 = min(T, t0 + rq);
   const bool dora = g != nullptr;
   float gv[4] = {1.f, 1.f, 1.f, 1.f}, inv[4] = {1.f, 1.f, 1.f, 1.f}, bv[4] = {0.f, 0.f, 0.f, 0.f};
   if (dora && col_ok) {
@@ -160,7 +161,12 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
     }
   }
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int tb = t0; tb < t1 && col_ok; tb += 4) {
+  // grid-stride over chunks of kGateRows rows (thread y: four consecutive rows of a chunk), so a
+  // grid of about two blocks per SM covers any T with one dg atomic per column and block
+  const int nchunk = (T + kGateRows - 1) / kGateRows;
+  for (int ch = blockIdx.y; ch < nchunk && col_ok; ch += gridDim.y) {
+    const int tb = ch * kGateRows + 4 * threadIdx.y, t1 = min(T, tb + 4);
+    if (tb >= t1) continue;
     float4 gt[4], av[4], yv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -548,11 +554,12 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
 int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
                   const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
   if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
-  if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "gate: too many rows"; return 1; }
+  const unsigned gx_blocks = (unsigned)((D / 4 + 127) / 128), nchunk = (unsigned)((T + kGateRows - 1) / kGateRows);
+  const unsigned gy = std::max(1u, std::min(nchunk, (unsigned)(2 * c->sm_count) / gx_blocks));
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "gate_bwd_dz");
-  launch_pdl(c, gate_bwd_dz_kernel, dim3((unsigned)((D / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)),
-             dim3(128, 4), 0, gx, gate, gstride, T, D, tps, y, bias, g, dz, dg);
+  launch_pdl(c, gate_bwd_dz_kernel, dim3(gx_blocks, gy), dim3(128, 4), 0, gx, gate, gstride, T, D, tps, y, bias, g, dz,
+             dg);
   return check_launch("gate_bwd_dz", err);
 }
 

@@ -25,6 +25,7 @@ enum DevError : int {
 };
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s: kernels here run for < 10 ms
+constexpr uint32_t kWaitSleepNs = 1000;   // suspend hint of one barrier poll in the warp-wide waits
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -74,6 +75,21 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+
+// try_wait with an explicit suspend-time hint: a waiting warp sleeps until the phase completes or
+// about `ns` nanoseconds pass, instead of re-polling the barrier back to back (the polls compete
+// with the working warps of the SM for issue and shared-memory slots)
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -192,13 +208,16 @@ struct WaiterW {
   __device__ __forceinline__ bool probe(uint32_t a, uint32_t parity) const {
     return CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait(a, parity);
   }
+  __device__ __forceinline__ bool probe_sleep(uint32_t a, uint32_t parity) const {
+    return CLUSTER ? mbar_try_wait_cluster(a, parity) : mbar_try_wait_sleep(a, parity, kWaitSleepNs);
+  }
   __device__ __forceinline__ bool operator()(uint64_t* bar, uint32_t parity, int code) const {
     const uint32_t a = smem_u32(bar);
     if (__all_sync(0xffffffffu, probe(a, parity))) return true;   // fast path: already complete
     if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
     const unsigned long long t0 = globaltimer();
     for (uint32_t i = 0;; ++i) {
-      if (__all_sync(0xffffffffu, probe(a, parity))) return true;
+      if (__all_sync(0xffffffffu, probe_sleep(a, parity))) return true;
       if ((i & 63u) == 63u) {
         if (__any_sync(0xffffffffu, *abort_flag != 0)) return false;
         if (__any_sync(0xffffffffu, globaltimer() - t0 > kWaitLimitNs)) {
