@@ -835,7 +835,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   uint8_t* sK = smem;
   uint8_t* sV = smem + 16384;
   uint8_t* sQd = smem + 32768;
-  float* s_ld = reinterpret_cast<float*>(smem + 32768 + NSTAGE * 16384);   // [2 groups][2 bufs][lse 64 | D 64]
+  // [2 groups][2 bufs][32 query pairs][lse 2 | D 2]: one 16-byte broadcast read per pair
+  float* s_ld = reinterpret_cast<float*>(smem + 32768 + NSTAGE * 16384);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 32768 + NSTAGE * 16384 + 2048);
   uint64_t* kv_full = bars;
   uint64_t* q_full = bars + 1;
@@ -960,8 +961,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     for (int i = g; i < nqt; i += 2, ++it) {
       const int q0 = (qt0 + i) * 64;
       float* lse_b = s_ld + 256 * g + 128 * (it & 1);
-      float* D_b = lse_b + 64;
-      lse_b[t] = next;               // lse_b[64 + c] is D_b[c]
+      lse_b[4 * ((t & 63) >> 1) + (t >= 64 ? 2 : 0) + (t & 1)] = next;
       if (i + 2 < nqt) next = fetch(i + 2);
       if (g == 0) named_bar(1, 128);   // every warp of the group passes it once per tile, also after an abort
       else named_bar(2, 128);
@@ -971,8 +971,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const uint32_t tS = tbase + 128 * (i % 3);
       const bool edge = !tile_visible(k0, 128, q0, 64, a.Sq, a.window) || kj >= a.Sk;
       const uint64_t sc2 = f2(a.sl2, a.sl2);
-      const float2* lse2 = reinterpret_cast<const float2*>(lse_b);
-      const float2* D2 = reinterpret_cast<const float2*>(D_b);
+      const float4* ld4 = reinterpret_cast<const float4*>(lse_b);
       // two halves of 32 queries: S^T / dP^T of a half in, its P^T / dS^T (packed bf16) out to the
       // first 16 columns of the half's slot (the packed halves never overlap columns still to read),
       // so about 100 values per thread are live instead of 192
@@ -991,7 +990,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         uint32_t pk[16], dk[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float2 lz = lse2[16 * hf + e], dz = D2[16 * hf + e];      // smem broadcast reads
+          const float4 w4 = ld4[16 * hf + e];      // smem broadcast read: lse and D of queries 2e, 2e + 1
+          const float2 lz = make_float2(w4.x, w4.y), dz = make_float2(w4.z, w4.w);
           float x0, x1, d0, d1;
           f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, f2(-lz.x, -lz.y)), x0,
                   x1);
