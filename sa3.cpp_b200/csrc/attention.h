@@ -87,8 +87,8 @@ int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gate_stride, int
 int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err);
 
 // SwiGLU: f[T][2I] -> a[T][I] = f[:, :I] * silu(f[:, I:]) (bf16); backward da -> df (f32)
-int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err);
-int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err);
+// act = bf16(val * silu(gate)) of f = [val | gate] (bf16, rows of 2I)
+int k_swiglu_fwd(Ctx* c, const __nv_bfloat16* f, int T, int I, __nv_bfloat16* a, std::string& err);
 
 // silu in place (f32) and its f32 -> bf16 copy for a following GEMM
 int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err);

@@ -56,7 +56,8 @@ struct DitTarget {
 struct DitBlockAct {
   float *x = nullptr, *rstd_a = nullptr, *qkv = nullptr, *rq = nullptr, *rk = nullptr, *lse_a = nullptr;
   float *yo = nullptr, *x1 = nullptr, *rstd_c = nullptr, *qf = nullptr, *rcq = nullptr, *kvf = nullptr;
-  float *rck = nullptr, *lse_c = nullptr, *x2 = nullptr, *rstd_f = nullptr, *ff = nullptr, *yf = nullptr;
+  float *rck = nullptr, *lse_c = nullptr, *x2 = nullptr, *rstd_f = nullptr, *yf = nullptr;
+  __nv_bfloat16* ff = nullptr;   // ff.proj output [val | gate], bf16 (read by the SwiGLU forward and backward)
   float* mod = nullptr;
   __nv_bfloat16 *h_a = nullptr, *qkvb = nullptr, *oa = nullptr, *hc = nullptr, *cq = nullptr, *kvb = nullptr;
   __nv_bfloat16 *oc = nullptr, *hf = nullptr, *act = nullptr;
@@ -318,7 +319,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
         a.lse_a2 = f(B * Hh * S); a.lse_c2 = f(B * Hh * S); a.rq2 = f(M * Hh); a.rk2 = f(M * Hh); a.rcq2 = f(M * Hh);
         a.rck2 = f(MC * Hh);
       }
-      a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = f(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
+      a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = h(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
       a.mod = f(B * 6 * D);
       a.yc = m.tix.count(m.bname(l, "cross.out.weight")) ? f(M * D) : nullptr;
     }
@@ -621,7 +622,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_residual_norm(c, a.x1, tco ? a.yc : m.dtmp, nullptr, 0, (int)M, D, S, a.x2, g_ff, a.mod + 3 * D,
                         a.mod + 4 * D, ms, k.norm_eps, a.hf, a.rstd_f, err))
       return 1;
-    if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, a.ff, nullptr, err)) return 1;
+    if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, nullptr, a.ff, err)) return 1;
     if (k_swiglu_fwd(c, a.ff, (int)M, I, a.act, err)) return 1;
     if (lin_fwd(m, wfo, tf, b_fo, a.act, M, a.yf, nullptr, err)) return 1;
     if (l + 1 < k.depth) {
@@ -688,7 +689,8 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, dz_of(m, tp),
                         dg_of(m, tp), err))
       return 1;
-    if (lin_bwd(m, wfp, tp, b_fp, a.hf, a.ff, nullptr, M, m.dh, 0, nullptr, err)) return 1;
+    // (dz / dg come from the SwiGLU backward, so the f32 output y is not needed here)
+    if (lin_bwd(m, wfp, tp, b_fp, a.hf, nullptr, nullptr, M, m.dh, 0, nullptr, err)) return 1;
     if (m.need_mod && k_mod_grad_norm(c, m.dh, a.x2, a.rstd_f, g_ff, (int)M, D, S, ms, m.dgcond + 3 * D,
                                       m.dgcond + 4 * D, err))
       return 1;

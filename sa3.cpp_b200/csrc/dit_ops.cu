@@ -503,42 +503,25 @@ __global__ void sub_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_
 
 // SwiGLU over rows: f[t] = [val (I) | gate (I)], a[t] = val * silu(gate).  Grid (I / 4 / 256
 // column blocks, T rows): each thread owns 4 consecutive columns of one row (128-bit accesses).
-__global__ void swiglu_fwd_kernel(const float* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
+// act = bf16(val * silu(gate)) of the ff.proj output f = [val | gate] (bf16 rows of 2I), eight
+// columns per thread (16-byte loads and stores)
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
   pdl_prologue();
-  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  const int j = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
-  const float* fr = f + (long)t * 2 * I;
-  const float4 v = *reinterpret_cast<const float4*>(fr + j);
-  const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
-  uint2 pk;
-  pk.x = pack_bf16x2(v.x * gl.x * sigm(gl.x), v.y * gl.y * sigm(gl.y));
-  pk.y = pack_bf16x2(v.z * gl.z * sigm(gl.z), v.w * gl.w * sigm(gl.w));
-  *reinterpret_cast<uint2*>(a + (long)t * I + j) = pk;
-  }
-}
-
-__global__ void swiglu_bwd_kernel(const float* __restrict__ da, const float* __restrict__ f, int T, int I,
-                                  float* __restrict__ df) {
-  pdl_prologue();
-  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
-  if (j >= I) return;
-  for (int t = blockIdx.y; t < T; t += gridDim.y) {
-  const float* fr = f + (long)t * 2 * I;
-  const float4 v = *reinterpret_cast<const float4*>(fr + j);
-  const float4 gl = *reinterpret_cast<const float4*>(fr + I + j);
-  const float4 d = *reinterpret_cast<const float4*>(da + (long)t * I + j);
-  const float vv[4] = {v.x, v.y, v.z, v.w}, gg[4] = {gl.x, gl.y, gl.z, gl.w}, dd[4] = {d.x, d.y, d.z, d.w};
-  float dv[4], dgl[4];
+    const __nv_bfloat16* fr = f + (long)t * 2 * I;
+    const uint4 v4 = *reinterpret_cast<const uint4*>(fr + j);
+    const uint4 g4 = *reinterpret_cast<const uint4*>(fr + I + j);
+    const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w}, gw[4] = {g4.x, g4.y, g4.z, g4.w};
+    uint32_t o[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float sg = sigm(gg[e]);
-    dv[e] = dd[e] * gg[e] * sg;
-    dgl[e] = dd[e] * vv[e] * sg * (1.f + gg[e] * (1.f - sg));
-  }
-  float* dr = df + (long)t * 2 * I;
-  *reinterpret_cast<float4*>(dr + j) = make_float4(dv[0], dv[1], dv[2], dv[3]);
-  *reinterpret_cast<float4*>(dr + I + j) = make_float4(dgl[0], dgl[1], dgl[2], dgl[3]);
+    for (int k = 0; k < 4; ++k) {
+      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[k]));
+      const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[k]));
+      o[k] = pack_bf16x2(v.x * g.x * sigm(g.x), v.y * g.y * sigm(g.y));
+    }
+    *reinterpret_cast<uint4*>(a + (long)t * I + j) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -790,18 +773,12 @@ int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::strin
   return check_launch("add", err);
 }
 
-int k_swiglu_fwd(Ctx* c, const float* f, int T, int I, __nv_bfloat16* a, std::string& err) {
+int k_swiglu_fwd(Ctx* c, const __nv_bfloat16* f, int T, int I, __nv_bfloat16* a, std::string& err) {
   ProfScope prof_(c, "swiglu_fwd");
-  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
-  launch_pdl(c, swiglu_fwd_kernel, dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, f, T, I, a);
+  if (I % 8) { err = "swiglu: the hidden width must be a multiple of 8"; return 1; }
+  launch_pdl(c, swiglu_fwd_kernel, dim3((unsigned)((I / 8 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0,
+             f, T, I, a);
   return check_launch("swiglu_fwd", err);
-}
-
-int k_swiglu_bwd(Ctx* c, const float* da, const float* f, int T, int I, float* df, std::string& err) {
-  ProfScope prof_(c, "swiglu_bwd");
-  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
-  launch_pdl(c, swiglu_bwd_kernel, dim3((unsigned)((I / 4 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0, da, f, T, I, df);
-  return check_launch("swiglu_bwd", err);
 }
 
 int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err) {
