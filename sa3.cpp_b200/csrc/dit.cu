@@ -110,7 +110,7 @@ struct DitModel {
   __nv_bfloat16 *xT_b = nullptr, *pout_b = nullptr;
   float *pout = nullptr, *vel = nullptr, *dvel = nullptr, *loss = nullptr, *dp = nullptr, *dxT = nullptr;
   // backward temporaries
-  float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dact = nullptr, *dq3 = nullptr, *Dsum = nullptr;
+  float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dq3 = nullptr, *Dsum = nullptr;
   float* dv2 = nullptr;   // differential: dV of the second softmax stream (run on +dO)
   // forward outputs kept for the backward of head / tail adapters (linear output without the
   // residual it is added to)
@@ -121,7 +121,7 @@ struct DitModel {
   float *dqf = nullptr, *dkv = nullptr, *dkvf = nullptr, *dvc2 = nullptr, *dctx = nullptr, *dmlp = nullptr;
   float *dgcond = nullptr, *dgsum = nullptr, *dxin0 = nullptr, *dxp = nullptr;
   bool need_ctx = false, need_mod = false, need_x0 = false;
-  __nv_bfloat16* dO_b = nullptr;
+  __nv_bfloat16 *dO_b = nullptr, *dact_b = nullptr;   // dact_b: the SwiGLU output gradient, bf16
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
   __nv_bfloat16 *dut = nullptr, *dz = nullptr, *cb = nullptr;
@@ -334,7 +334,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     m.xT_b = h(MT * D); m.pout_b = h(MT * k.io); m.pout = f(MT * k.io); m.vel = f(MT * k.io); m.dvel = f(MT * k.io);
     m.loss = f(64); m.dp = f(MT * k.io); m.dxT = f(MT * D);
     const int64_t wide = std::max<int64_t>(std::max<int64_t>(Q, 2 * I), D);
-    m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact = f(M * I); m.dq3 = f(M * Q);
+    m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact_b = h(M * I); m.dq3 = f(M * Q);
     m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
     m.dv2 = diff ? f(M * D) : nullptr;
     m.pre_lin = f(MT * k.io); m.vel_lin = f(MT * k.io); m.g_y = f(B * D); m.ctx_y = f(MC * D);
@@ -685,8 +685,8 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_gate_bwd_dz(c, m.gx, a.mod + 5 * D, ms, (int)M, D, S, a.yf, b_fo, tf && tf->prep.dora() ? tf->prep.g : nullptr,
                       dz_of(m, tf), dg_of(m, tf), err))
       return 1;
-    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, m.dact, 0, nullptr, err)) return 1;
-    if (k_swiglu_bwd_dz(c, m.dact, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, dz_of(m, tp),
+    if (lin_bwd(m, wfo, tf, b_fo, a.act, a.yf, nullptr, M, nullptr, 0, m.dact_b, err)) return 1;
+    if (k_swiglu_bwd_dz(c, m.dact_b, a.ff, (int)M, I, b_fp, tp && tp->prep.dora() ? tp->prep.g : nullptr, dz_of(m, tp),
                         dg_of(m, tp), err))
       return 1;
     // (dz / dg come from the SwiGLU backward, so the f32 output y is not needed here)

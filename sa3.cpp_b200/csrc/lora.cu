@@ -208,8 +208,8 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
   }
 }
 
-// SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (bf16), da the
-// gradient of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I
+// SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (bf16), da (bf16)
+// the gradient of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I
 // columns).  Thread = 4 columns of val and the matching 4 of gate, block = kFuseTok rows (two
 // rows' loads first); dz = bf16(g dy) and, for DoRA, dg += colsum(dy (y - bias) / g).
 __device__ __forceinline__ void bf16x4(const uint2 w, float (&v)[4]) {
@@ -218,7 +218,8 @@ __device__ __forceinline__ void bf16x4(const uint2 w, float (&v)[4]) {
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
 
-__global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const __nv_bfloat16* __restrict__ f, int T, int I,
+__global__ void swiglu_bwd_dz_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ f, int T,
+                                     int I,
                                      const float* __restrict__ bias, const float* __restrict__ g,
                                      __nv_bfloat16* __restrict__ dz, float* __restrict__ dg) {
   pdl_prologue();
@@ -240,24 +241,23 @@ __global__ void swiglu_bwd_dz_kernel(const float* __restrict__ da, const __nv_bf
   }
   float accv[4] = {0.f, 0.f, 0.f, 0.f}, accg[4] = {0.f, 0.f, 0.f, 0.f};
   for (int tb = t0; tb < t1; tb += 2) {
-    uint2 v2[2], g2[2];
-    float4 d2[2];
+    uint2 v2[2], g2[2], d2[2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {                    // both rows' loads first
       const int t = min(tb + u, t1 - 1);
       const __nv_bfloat16* fr = f + (long)t * 2 * I;
       v2[u] = *reinterpret_cast<const uint2*>(fr + j);
       g2[u] = *reinterpret_cast<const uint2*>(fr + I + j);
-      d2[u] = *reinterpret_cast<const float4*>(da + (long)t * I + j);
+      d2[u] = *reinterpret_cast<const uint2*>(da + (long)t * I + j);
     }
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const int t = tb + u;
       if (t >= t1) break;
-      float vv[4], gg[4];
+      float vv[4], gg[4], dd[4];
       bf16x4(v2[u], vv);
       bf16x4(g2[u], gg);
-      const float dd[4] = {d2[u].x, d2[u].y, d2[u].z, d2[u].w};
+      bf16x4(d2[u], dd);
       float dv[4], dgl[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -574,7 +574,8 @@ int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int 
   return check_launch("gate_bwd_dz", err);
 }
 
-int k_swiglu_bwd_dz(Ctx* c, const float* da, const __nv_bfloat16* f, int T, int I, const float* bias, const float* g,
+int k_swiglu_bwd_dz(Ctx* c, const __nv_bfloat16* da, const __nv_bfloat16* f, int T, int I, const float* bias,
+                    const float* g,
                     __nv_bfloat16* dz, float* dg, std::string& err) {
   if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }

@@ -42,8 +42,8 @@ int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, 
 // dz = bf16(g * dy) and dg = colsum(dy * (y - bias) / g) (dg zeroed first; g null: dz = bf16(dy)).
 int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
                   const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err);
-int k_swiglu_bwd_dz(Ctx* c, const float* da, const __nv_bfloat16* f, int T, int I, const float* bias, const float* g,
-                    __nv_bfloat16* dz, float* dg, std::string& err);
+int k_swiglu_bwd_dz(Ctx* c, const __nv_bfloat16* da, const __nv_bfloat16* f, int T, int I, const float* bias,
+                    const float* g, __nv_bfloat16* dz, float* dg, std::string& err);
 int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
                    int64_t out, __nv_bfloat16* dz, float* dg, std::string& err);
 int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
