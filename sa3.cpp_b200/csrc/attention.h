@@ -58,6 +58,9 @@ struct HeadSlice {
 };
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
                     int tokens_per_sample, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err);
+// the same with bf16 projection rows
+int k_head_prep_fwd(Ctx* c, const __nv_bfloat16* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                    int tokens_per_sample, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err);
 // Backward of one slice: g[T][H*64] (f32, gradient w.r.t. the prepared slice) -> dy slice of
 // dy[T][ncols] (f32, overwritten; or, with dy_bf, written as bf16 there instead), using the
 // forward input y and the saved rstd.
@@ -67,10 +70,10 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
                     const float* g2 = nullptr, long g2_ld = 0);
 // Self-attention q/k/v head preparation backward (dq3 = [dq | dk | dv] f32, or with nsl = 5 the
 // differential layout [dq | dk | dv | dqd | dkd] whose second stream ran on +dO, dv2 its dV, and
-// rq2 / rk2 its rstd; qkv = the projection output) fused with the qkv projection's backward
+// rq2 / rk2 its rstd; qkv = the projection output, bf16) fused with the qkv projection's backward
 // prologue: dz = bf16(g * dy) [T][nsl D] and dg = colsum(dy * qkv / g) (DoRA g; null: plain bf16
 // conversion, dg untouched).
-int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, int nsl, const float* rq,
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __nv_bfloat16* qkv, int T, int D, int H, int nsl, const float* rq,
                  const float* rk, const float* rq2, const float* rk2, const float* dv2, const float* gq,
                  const float* gk, int tokens_per_sample, int rot, float rope_base, const float* g,
                  __nv_bfloat16* dz, float* dg, std::string& err);

@@ -54,7 +54,8 @@ struct DitTarget {
 };
 
 struct DitBlockAct {
-  float *x = nullptr, *rstd_a = nullptr, *qkv = nullptr, *rq = nullptr, *rk = nullptr, *lse_a = nullptr;
+  float *x = nullptr, *rstd_a = nullptr, *rq = nullptr, *rk = nullptr, *lse_a = nullptr;
+  __nv_bfloat16* qkv = nullptr;   // qkv projection output, bf16 (read by the head preparation and its backward)
   float *yo = nullptr, *x1 = nullptr, *rstd_c = nullptr, *qf = nullptr, *rcq = nullptr, *kvf = nullptr;
   float *rck = nullptr, *lse_c = nullptr, *x2 = nullptr, *rstd_f = nullptr, *yf = nullptr;
   __nv_bfloat16* ff = nullptr;   // ff.proj output [val | gate], bf16 (read by the SwiGLU forward and backward)
@@ -310,7 +311,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     m.blk.assign(k.depth, DitBlockAct{});
     for (int l = 0; l < k.depth; ++l) {
       DitBlockAct& a = m.blk[l];
-      a.x = f(M * D); a.rstd_a = f(M); a.h_a = h(M * D); a.qkv = f(M * Q); a.qkvb = h(M * Q);
+      a.x = f(M * D); a.rstd_a = f(M); a.h_a = h(M * D); a.qkv = h(M * Q); a.qkvb = h(M * Q);
       a.rq = f(M * Hh); a.rk = f(M * Hh); a.oa = h(M * D); a.lse_a = f(B * Hh * S); a.yo = f(M * D);
       a.x1 = f(M * D); a.rstd_c = f(M); a.hc = h(M * D); a.qf = f(M * Dq); a.cq = h(M * Dq); a.rcq = f(M * Hh);
       a.kvf = f(MC * Dk); a.kvb = h(MC * Dk); a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
@@ -566,7 +567,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (l == 0 &&
         k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err))
       return 1;
-    if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, a.qkv, nullptr, err)) return 1;
+    if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, nullptr, a.qkv, err)) return 1;
     {
       // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE
       HeadSlice hs[5];
@@ -781,7 +782,8 @@ static int dit_step(DitModel& m, std::string& err) {
                      k.rot, k.rope_base, tq && tq->prep.dora() ? tq->prep.g : nullptr, dz_of(m, tq), dg_of(m, tq),
                      err))
       return 1;
-    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, a.qkv, nullptr, M, m.dh, 0, nullptr, err)) return 1;
+    // (dz / dg come from the fused head backward, so the f32 output y is not needed here)
+    if (lin_bwd(m, wqkv, tq, nullptr, a.h_a, nullptr, nullptr, M, m.dh, 0, nullptr, err)) return 1;
     if (m.need_mod && k_mod_grad_norm(c, m.dh, a.x, a.rstd_a, g_pre, (int)M, D, S, ms, m.dgcond, m.dgcond + D, err))
       return 1;
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x, a.rstd_a, (int)M, D, g_pre, a.mod, ms, S, m.gx, nullptr, err)) return 1;

@@ -52,6 +52,17 @@ __device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 w = *reinterpret_cast<const uint4*>(p);
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[k]));
+    v[2 * k] = f.x;
+    v[2 * k + 1] = f.y;
+  }
+}
+
 __device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
@@ -232,7 +243,8 @@ __device__ __forceinline__ void rope8(float (&v)[8], int j, int pos, int rot, co
 }
 
 // Grid (ceil(H * nslices / 8), ceil(T / kHpRows)).
-__global__ void __launch_bounds__(256) head_prep_fwd_kernel(const float* __restrict__ y, int T, int ncols, int H,
+template <typename Y>
+__global__ void __launch_bounds__(256) head_prep_fwd_kernel(const Y* __restrict__ y, int T, int ncols, int H,
                                                             const HeadSlices slices, int tps, float eps, int rot,
                                                             const float2* __restrict__ tab,
                                                             __nv_bfloat16* __restrict__ out) {
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
 // stream run on +dO, so they enter negated, and the v gradient is dq3's minus dv2 (that
 // stream's dV).  Grid (ceil(nsl H / 8), ceil(T / kHpRows)).
 __global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
-                                                            const float* __restrict__ qkv, int T, int D, int H,
+                                                            const __nv_bfloat16* __restrict__ qkv, int T, int D, int H,
                                                             int nsl, const float* __restrict__ rq,
                                                             const float* __restrict__ rk, const float* __restrict__ rq2,
                                                             const float* __restrict__ rk2, const float* __restrict__ dv2,
@@ -380,31 +392,32 @@ __global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restr
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
   const int tb0 = blockIdx.y * kQkvRows;
   int pos = (tb0 + q) % tps;
-  // rows in pairs, both rows' loads issued before either is used (the dz stores in between may
+  // the next row's loads are issued before this row is processed (the dz stores in between may
   // alias the inputs for the compiler)
-  float gvr[2][8], yvr[2][8], rr[2];
-#pragma unroll 1
-  for (int it0 = 0; it0 < kQkvRows / 4 && tb0 + 4 * it0 < T; it0 += 2) {
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int t = tb0 + 4 * (it0 + u) + q;
-    rr[u] = 0.f;
-    if (t < T) {
-      ld8(dq3 + (long)t * ncols + col, gvr[u]);
-      if (norm || g) ld8(qkv + (long)t * ncols + col, yvr[u]);
-      if (norm) rr[u] = rs[(long)t * H + h];
+  float gvn[8], yvn[8], rn = 0.f;
+  auto fetch = [&](int it) {
+    const int t = tb0 + 4 * it + q;
+    rn = 0.f;
+    if (it < kQkvRows / 4 && t < T) {
+      ld8(dq3 + (long)t * ncols + col, gvn);
+      if (norm || g) ld8(qkv + (long)t * ncols + col, yvn);
+      if (norm) rn = rs[(long)t * H + h];
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) gvr[u][k] = yvr[u][k] = 0.f;
+      for (int k = 0; k < 8; ++k) gvn[k] = yvn[k] = 0.f;
     }
-  }
-#pragma unroll
-  for (int u = 0; u < 2; ++u) {
-    const int t = tb0 + 4 * (it0 + u) + q;
+  };
+  fetch(0);
+#pragma unroll 1
+  for (int it = 0; it < kQkvRows / 4 && tb0 + 4 * it < T; ++it) {
+  {
+    const int t = tb0 + 4 * it + q;
     const bool valid = t < T;
-    float (&gv)[8] = gvr[u];
-    const float (&yv)[8] = yvr[u];
-    const float r = rr[u];
+    float gv[8], yv[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) gv[k] = gvn[k], yv[k] = yvn[k];
+    const float r = rn;
+    fetch(it + 1);
     if (valid && sub_dv2) {
       float w[8];
       ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
@@ -697,8 +710,9 @@ static const float2* rope_table(Ctx* c, int tps, int rot, float rope_base, std::
   return static_cast<const float2*>(tab);
 }
 
-int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
-                    float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+template <typename Y>
+static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
+                           float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
   if (rot != 0 && rot != 32 && rot != 64) { err = "rope: rot must be 32 or 64"; return 1; }
   if (nslices < 1 || nslices > 5) { err = "head_prep: 1..5 slices"; return 1; }
   HeadSlices hs{};
@@ -713,11 +727,21 @@ int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadS
   ProfScope prof_(c, "head_prep_fwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
-  launch_pdl(c, head_prep_fwd_kernel, grid, 256, 0, y, T, ncols, H, hs, tps, eps, rot, tab, out);
+  launch_pdl(c, head_prep_fwd_kernel<Y>, grid, 256, 0, y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
 
-int k_qkv_bwd_dz(Ctx* c, const float* dq3, const float* qkv, int T, int D, int H, int nsl, const float* rq,
+int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
+                    float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+  return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err);
+}
+
+int k_head_prep_fwd(Ctx* c, const __nv_bfloat16* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                    int tps, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+  return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err);
+}
+
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __nv_bfloat16* qkv, int T, int D, int H, int nsl, const float* rq,
                  const float* rk, const float* rq2, const float* rk2, const float* dv2, const float* gq, const float* gk,
                  int tps, int rot, float rope_base, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
   if (nsl != 3 && nsl != 5) { err = "qkv backward: 3 or 5 slices"; return 1; }
