@@ -73,6 +73,13 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       drains (each kernel waits for its predecessor's results before reading them; captured
  *       graphs keep plain edges, which replay faster); 0: plain stream order always. */
 #define SA3K_OPT_PDL 6
+/* SA3K_OPT_STEP_GRAPH  1 (default): sa3k_dit_forward_backward records the step as a CUDA graph on
+ *       its second call at a given (B, T, ctx_len) and replays it from then on (one launch per
+ *       call instead of ~1000).  The graph is dropped and re-recorded after anything it depends on
+ *       changes: tensors, adapters, context options or the context's scratch buffers.  Calls made
+ *       while the stream is being captured, or with profiling timing on, run eagerly.
+ *       0: every call launches its kernels one by one. */
+#define SA3K_OPT_STEP_GRAPH 7
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded
@@ -296,7 +303,8 @@ int sa3k_dit_adapter_copy(sa3k_dit* dit, int which, float* buf, int64_t offset, 
 /* Zero the accumulated gradients (train_clear_accum, src/train_loop.h:80-82). */
 int sa3k_dit_zero_grads(sa3k_dit* dit, char* err, int err_len);
 
-/* Forward + backward of B samples of T frames: x_t, target [B][T][io]; t_feat [B][time_dim]
+/* Forward + backward of B samples of T frames (replayed from a recorded CUDA graph, see
+ * SA3K_OPT_STEP_GRAPH): x_t, target [B][T][io]; t_feat [B][time_dim]
  * (expo_features, src/sa3_pipeline.h:57-67); cross [B][ctx_len][cond_dim]; global [B][cond_dim]
  * (host or device pointers).  Adds the adapter gradients of the summed per-sample losses to the
  * accumulated gradients and writes the B per-sample losses (mean squared error over io*T) to

@@ -26,6 +26,7 @@ void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err) {
   if ((int)c->scratch.size() <= slot) c->scratch.resize((size_t)slot + 1);
   Scratch& s = c->scratch[(size_t)slot];
   if (s.bytes < bytes) {
+    ++c->gen;   // recorded graphs may hold the old buffer
     if (s.ptr) {
       cudaStreamSynchronize(c->stream);
       cudaFree(s.ptr);
@@ -242,6 +243,7 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* stream, char* err, int err_len) {
 
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len) {
   if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  ++ctx->c.gen;
   switch (option) {
     case SA3K_OPT_WEIGHT_BF16_CACHE: ctx->c.weight_cache = value != 0; return 0;
     case SA3K_OPT_SMEM_DEQUANT: ctx->c.smem_dequant = value != 0; return 0;
@@ -256,6 +258,7 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
       return 0;
     case SA3K_OPT_ATTN_TC: ctx->c.attn_tc = value != 0; return 0;
     case SA3K_OPT_PDL: ctx->c.pdl = value != 0; return 0;
+    case SA3K_OPT_STEP_GRAPH: ctx->c.step_graph = value != 0; return 0;
     default: return fill_err(err, err_len, "unknown option");
   }
 }

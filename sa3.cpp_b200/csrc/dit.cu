@@ -128,7 +128,22 @@ struct DitModel {
   __nv_bfloat16 *dut = nullptr, *dz = nullptr, *cb = nullptr;
   int64_t ut_ld = 0;
 
+  // the step recorded as a CUDA graph (SA3K_OPT_STEP_GRAPH): valid for shape (gB, gT, gC) while
+  // the context generation is g_cgen and the model generation g_mgen; launch counts per profile
+  // class of one replay (so the context's launch counters stay true)
+  uint64_t gen = 0;                                 // bumped by set_tensor / init_adapters
+  cudaGraphExec_t step_exec = nullptr;
+  int gB = 0, gT = 0, gC = 0;
+  uint64_t g_cgen = 0, g_mgen = 0;
+  std::vector<std::pair<std::string, long long>> g_launches;
+  cudaStream_t cap_stream = nullptr;                // private stream the graph is recorded on
+  bool warm = false;                                // one eager call at the current key done
+  int wB = 0, wT = 0, wC = 0;
+  uint64_t w_cgen = 0, w_mgen = 0;
+
   ~DitModel() {
+    if (step_exec) cudaGraphExecDestroy(step_exec);
+    if (cap_stream) cudaStreamDestroy(cap_stream);
     r16_group_free(r16_prep);
     r16_group_free(r16_grads);
     for (void* q : owned) cudaFree(q);
@@ -831,6 +846,80 @@ static int dit_step(DitModel& m, std::string& err) {
   return 0;
 }
 
+// The step through its recorded CUDA graph where that is possible: the first call at a shape (and
+// context / model generation) runs eagerly and allocates everything, the second records the
+// graph and replays it, later ones only replay.  A stream that is being captured (the caller
+// records its own graph), profiling timing, or a failed recording runs the step eagerly.
+static int run_step(DitModel& m, std::string& err) {
+  Ctx* c = m.c;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess) cudaGetLastError();
+  if (!c->step_graph || c->timing || cs != cudaStreamCaptureStatusNone) return dit_step(m, err);
+  if (m.step_exec && m.gB == m.B && m.gT == m.T && m.gC == m.C && m.g_cgen == c->gen && m.g_mgen == m.gen) {
+    if (cudaGraphLaunch(m.step_exec, c->stream) != cudaSuccess) return check_launch("step graph", err);
+    for (const auto& pl : m.g_launches) {
+      auto it = std::find_if(c->prof.begin(), c->prof.end(), [&](const ProfEntry& e) { return e.name == pl.first; });
+      if (it == c->prof.end()) {
+        c->prof.emplace_back();
+        c->prof.back().name = pl.first;
+        it = c->prof.end() - 1;
+      }
+      it->launches += pl.second;
+    }
+    return 0;
+  }
+  if (m.step_exec) {
+    cudaGraphExecDestroy(m.step_exec);
+    m.step_exec = nullptr;
+  }
+  const bool same = m.warm && m.wB == m.B && m.wT == m.T && m.wC == m.C && m.w_cgen == c->gen && m.w_mgen == m.gen;
+  if (!same) {   // first call at this key: eager (allocations, caches)
+    const int rc = dit_step(m, err);
+    m.warm = rc == 0;
+    m.wB = m.B; m.wT = m.T; m.wC = m.C; m.w_cgen = c->gen; m.w_mgen = m.gen;
+    return rc;
+  }
+  // recorded on a private stream (the caller's may be the legacy default stream, which cannot
+  // be captured); the graph is then launched on the caller's stream
+  if (!m.cap_stream && cudaStreamCreateWithFlags(&m.cap_stream, cudaStreamNonBlocking) != cudaSuccess) {
+    cudaGetLastError();
+    m.cap_stream = nullptr;
+    return dit_step(m, err);
+  }
+  std::vector<long long> before(c->prof.size());
+  for (size_t i = 0; i < c->prof.size(); ++i) before[i] = c->prof[i].launches;
+  const cudaStream_t user = c->stream;
+  if (cudaStreamBeginCapture(m.cap_stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    cudaGetLastError();
+    return dit_step(m, err);
+  }
+  c->stream = m.cap_stream;
+  std::string e2;
+  const int rc = dit_step(m, e2);
+  c->stream = user;
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(m.cap_stream, &g);
+  cudaGraphExec_t exec = nullptr;
+  const bool ok = rc == 0 && ce == cudaSuccess && g && cudaGraphInstantiate(&exec, g, 0) == cudaSuccess;
+  if (g) cudaGraphDestroy(g);
+  if (!ok) {   // nothing recorded ran: run the step eagerly and stay eager at this key
+    cudaGetLastError();
+    if (exec) cudaGraphExecDestroy(exec);
+    m.warm = false;
+    for (size_t i = 0; i < c->prof.size() && i < before.size(); ++i) c->prof[i].launches = before[i];
+    return dit_step(m, err);
+  }
+  m.g_launches.clear();
+  for (size_t i = 0; i < c->prof.size(); ++i) {
+    const long long d = c->prof[i].launches - (i < before.size() ? before[i] : 0);
+    if (d) m.g_launches.emplace_back(c->prof[i].name, d);
+  }
+  m.step_exec = exec;
+  m.gB = m.B; m.gT = m.T; m.gC = m.C; m.g_cgen = c->gen; m.g_mgen = m.gen;
+  if (cudaGraphLaunch(exec, c->stream) != cudaSuccess) return check_launch("step graph", err);
+  return 0;
+}
+
 }  // namespace sa3k
 
 using namespace sa3k;
@@ -924,6 +1013,7 @@ int sa3k_dit_set_tensor(sa3k_dit* d, const char* name, int type, const void* hos
   DitModel& m = d->m;
   cudaSetDevice(m.c->device);
   const std::string n(name);
+  ++m.gen;
   int64_t x0 = 0, x1 = 0;
   if (!dit_tensor_shape(m.cfg, n, x0, x1)) return dfail(err, err_len, "not a tensor of this DiT: " + n);
   if (ne0 != x0 || (ne1 > 0 ? ne1 : 1) != x1)
@@ -958,6 +1048,7 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
   if (at != "lora" && at != "dora-rows") return dfail(err, err_len, "adapter type must be lora or dora-rows");
   if (rank < 1 || rank > 16) return dfail(err, err_len, "rank must be 1..16");
   if (!m.tg.empty()) return dfail(err, err_len, "adapters already initialised");
+  ++m.gen;
   m.dora = at == "dora-rows";
   m.rank = rank;
   m.alpha = alpha;
@@ -1085,7 +1176,7 @@ int sa3k_dit_forward_backward(sa3k_dit* d, int B, int T, int ctx_len, const floa
                             st) == cudaSuccess &&
             cudaMemcpyAsync(m.in_glob, global, sizeof(float) * B * k.cond_dim, cudaMemcpyDefault, st) == cudaSuccess;
   if (!ok) return dfail(err, err_len, "input copy failed");
-  if (dit_step(m, e)) return dfail(err, err_len, e);
+  if (run_step(m, e)) return dfail(err, err_len, e);
   if (loss && cudaMemcpyAsync(loss, m.loss, sizeof(float) * B, cudaMemcpyDefault, st) != cudaSuccess)
     return dfail(err, err_len, "loss copy failed");
   return 0;

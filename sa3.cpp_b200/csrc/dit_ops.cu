@@ -694,6 +694,7 @@ static const float2* rope_table(Ctx* c, int tps, int rot, float rope_base, std::
   void* tab = scratch_get(c, kSlotRope, bytes, err);
   if (!tab) return nullptr;
   if (tab != c->rope_tab || c->rope_tps != tps || c->rope_rot != rot || c->rope_base != rope_base) {
+    ++c->gen;   // recorded graphs may rely on the table's previous contents
     const int n = tps * (rot / 2);
     rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, c->stream>>>(tps, rot, log2f(rope_base),
                                                                             static_cast<float2*>(tab));

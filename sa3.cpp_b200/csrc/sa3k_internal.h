@@ -61,6 +61,10 @@ struct Ctx {
   int gemm_pair = 1;                 // CTA-pair (cta_group::2) GEMMs: 0 never, 1 where they pay, 2 always
   bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
   bool pdl = true;                   // programmatic dependent launch between consecutive kernels
+  bool step_graph = true;            // the DiT step records and replays a CUDA graph
+  // bumped whenever something a recorded graph may depend on changes: an option, a scratch
+  // buffer reallocated, the RoPE table rebuilt
+  uint64_t gen = 0;
   // NeoX RoPE (cos, sin) table for (positions, rot, base), kept in scratch slot kSlotRope
   const void* rope_tab = nullptr;
   int rope_tps = 0, rope_rot = 0;

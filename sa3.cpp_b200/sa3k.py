@@ -29,6 +29,7 @@ ABI_SYMBOLS = (
     "sa3k_dit_dp_apply_adamw",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
+OPT_STEP_GRAPH = 7
 
 
 class Sa3kError(RuntimeError):

@@ -190,3 +190,28 @@ def test_dit_rejects_misshaped_tensors(ctx):
         ok = (5 if diff else 3) * D
         dit.set_tensor("dit.0.self.qkv.weight", "f32", np.zeros((ok, D), np.float32), D, ok)
         dit.close()
+
+
+def test_step_graph_replay_matches_eager(ctx):
+    """sa3k_dit_forward_backward runs eagerly on its first call at a shape, records the step as a
+    CUDA graph on the second and replays it afterwards; every call must give the eager result
+    (up to the order of f32 atomic additions), and a changed context option re-records."""
+    import sa3k
+    ctx.set_option(sa3k.OPT_STEP_GRAPH, 1)
+    dit, deq, ad, targets, rng = _build(ctx, dict(CFG))
+    inputs = _inputs(rng)
+    res = []
+    for call in range(5):
+        if call == 3:
+            ctx.set_option(sa3k.OPT_PDL, 1)   # any option change drops the recorded graph
+        dit.zero_grads()
+        loss = np.zeros(B, np.float32)
+        dit.forward_backward(B, T, CTX, *inputs, loss=loss)
+        ctx.sync()
+        g = np.zeros(dit.size(), np.float32)
+        dit.copy(1, g, to_model=False)
+        res.append((loss, g))
+    for loss, g in res[1:]:
+        np.testing.assert_allclose(loss, res[0][0], rtol=1e-5)
+        assert rel_l2(g, res[0][1]) < 1e-5
+    dit.close()
