@@ -314,6 +314,67 @@ int sa3k_dit_forward_backward(sa3k_dit* dit, int B, int T, int ctx_len, const fl
                               const float* target, const float* t_feat, const float* cross,
                               const float* global, float* loss, char* err, int err_len);
 
+/* ---- adapter and trainer-state files (the reference's GGUF formats) ----
+ * Adapter file (write_train_lora_gguf / load_train_lora_gguf, src/train_checkpoint.h:42-173):
+ * metadata general.architecture "sa3-lora", lora.adapter_type, lora.rank, lora.alpha,
+ * lora.n_targets; per target <stem>.lora_A f32 ne {in, rank}, <stem>.lora_B ne {rank, out},
+ * <stem>.magnitude ne {out} (dora-rows), stem = the weight name without ".weight", targets in
+ * name order.  Such a file loads as an adapter in the reference's generator. */
+int sa3k_dit_save_adapter(sa3k_dit* dit, const char* path, char* err, int err_len);
+/* Adapter values from a file into the model's parameters (train_restore_adapter_values,
+ * src/train_resume.h:104-148): type, rank and alpha must equal the model's adapters, the file
+ * must hold exactly the model's targets with their shapes. */
+int sa3k_dit_load_adapter(sa3k_dit* dit, const char* path, char* err, int err_len);
+
+/* Dataset-side progress stored in the trainer-state file (TrainResumeProgress,
+ * src/train_resume.h:23-37): the trainer's epoch, cursor and sample order, its compatibility
+ * string and the serialized random-engine states of its samplers. */
+typedef struct sa3k_train_progress {
+  uint64_t epoch;
+  uint64_t next_sample;
+  const uint64_t* order;
+  int64_t n_order;
+  const char* compatibility;
+  const char* rng_shuffle;
+  const char* rng_crop;
+  const char* rng_cfg;
+  const char* rng_prompt;
+  const char* rng_inpaint;
+  const char* rng_diffusion;
+} sa3k_train_progress;
+
+/* Immutable checkpoint pair (write_train_checkpoint_pair, src/train_resume.h:502-538): the adapter
+ * file and a trainer-state file (general.architecture "sa3-trainer-state", trainer.* metadata,
+ * optimizer.<stem>.<lora_A|lora_B|magnitude>.<m|v> f32 AdamW moments) bound to the adapter by its
+ * FNV-1a fingerprint.  Refuses to overwrite either file; both are written to ".tmp" names and
+ * renamed, the state last.  `step` = the number of AdamW updates applied so far. */
+int sa3k_dit_save_checkpoint(sa3k_dit* dit, const char* adapter_path, const char* state_path, int64_t step,
+                             const sa3k_train_progress* progress, char* err, int err_len);
+/* Restores parameters and AdamW moments from a pair (load_train_state_gguf,
+ * src/train_resume.h:394-500): the adapter must match the state's fingerprint and the state's
+ * target inventory the model's; returns the step.  The dataset-side progress is read back with
+ * the sa3k_gguf_get_* calls below. */
+int sa3k_dit_load_checkpoint(sa3k_dit* dit, const char* adapter_path, const char* state_path, int64_t* step,
+                             char* err, int err_len);
+
+/* Host-only file helpers (no device needed). */
+/* An adapter file from host arrays (the same format as sa3k_dit_save_adapter); m may be NULL
+ * (plain LoRA) or hold NULL entries. */
+int sa3k_adapter_gguf_write(const char* path, const char* adapter_type, int rank, float alpha, int n,
+                            const char* const* stems, const int64_t* in, const int64_t* out, const float* const* A,
+                            const float* const* B, const float* const* m, char* err, int err_len);
+/* Metadata of a GGUF file: a string (copied NUL-terminated into buf, its length to len_out), an
+ * unsigned integer, an unsigned integer array (up to max elements, the count to n_out). */
+int sa3k_gguf_get_string(const char* path, const char* key, char* buf, int64_t buf_len, int64_t* len_out,
+                         char* err, int err_len);
+int sa3k_gguf_get_u64(const char* path, const char* key, uint64_t* value, char* err, int err_len);
+int sa3k_gguf_get_u64_array(const char* path, const char* key, uint64_t* out, int64_t max, int64_t* n_out,
+                            char* err, int err_len);
+/* An f32 tensor of a GGUF file (up to max values; the element count to n_out, dims to ne[4] and
+ * n_dims). */
+int sa3k_gguf_get_f32(const char* path, const char* name, float* out, int64_t max, int64_t* n_out, int64_t* ne,
+                      int* n_dims, char* err, int err_len);
+
 /* Average over `count` samples, clip, AdamW (train_apply_accumulated_adamw,
  * src/train_loop.h:173-211) on the flat state. */
 int sa3k_dit_apply_adamw(sa3k_dit* dit, int count, const sa3k_adamw_params* hp, int step,

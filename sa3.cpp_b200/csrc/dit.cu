@@ -23,14 +23,17 @@
 #include "../../include/sa3k.h"
 #include "attention.h"
 #include "gemm_r16.h"
+#include "gguf_io.h"
 #include "linear.h"
 #include "lora_kernels.h"
 
 #include <algorithm>
 #include <cmath>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <sys/stat.h>
 #include <string>
 #include <vector>
 
@@ -1195,6 +1198,272 @@ int sa3k_dit_dp_apply_adamw(sa3k_dit* d, sa3k_dp_comm* comm, int samples_per_ran
   DitModel& m = d->m;
   return sa3k_dp_allreduce_adamw(m.handle, comm, m.p, m.g, m.am, m.av, m.np, samples_per_rank, hp, step,
                                  grad_norm_out, err, err_len);
+}
+
+
+// ------------------------------------------------------------------ adapter / trainer-state files
+// Targets in the reference's order (enumerate_train_lora_targets sorts them by weight name,
+// src/train_lora.h:97-117), with their file stems (the weight name without ".weight").
+static std::vector<size_t> file_order(const DitModel& m) {
+  std::vector<size_t> o(m.tg.size());
+  for (size_t i = 0; i < o.size(); ++i) o[i] = i;
+  std::sort(o.begin(), o.end(), [&](size_t a, size_t b) { return m.tg[a].name < m.tg[b].name; });
+  return o;
+}
+
+static std::string stem_of(const std::string& n) {
+  return n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0 ? n.substr(0, n.size() - 7) : n;
+}
+
+static int fetch_flat(DitModel& m, const float* dev, std::vector<float>& host, std::string& err) {
+  host.assign((size_t)m.np, 0.f);
+  if (cudaStreamSynchronize(m.c->stream) != cudaSuccess ||
+      cudaMemcpy(host.data(), dev, sizeof(float) * (size_t)m.np, cudaMemcpyDeviceToHost) != cudaSuccess) {
+    cudaGetLastError();
+    err = "adapter state copy to the host failed";
+    return 1;
+  }
+  return 0;
+}
+
+static int store_flat(DitModel& m, float* dev, const std::vector<float>& host, std::string& err) {
+  if (cudaStreamSynchronize(m.c->stream) != cudaSuccess ||
+      cudaMemcpy(dev, host.data(), sizeof(float) * (size_t)m.np, cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    err = "adapter state copy to the device failed";
+    return 1;
+  }
+  return 0;
+}
+
+static std::string adapter_type_of(const DitModel& m) { return m.dora ? "dora-rows" : "lora"; }
+
+static int write_adapter_file(DitModel& m, const std::string& path, std::string& err) {
+  std::vector<float> p;
+  if (fetch_flat(m, m.p, p, err)) return 1;
+  std::vector<AdapterTargetView> v;
+  for (size_t i : file_order(m)) {
+    const DitTarget& t = m.tg[i];
+    AdapterTargetView a;
+    a.stem = stem_of(t.name);
+    a.in = t.in;
+    a.out = t.out;
+    a.A = p.data() + t.offA;
+    a.B = p.data() + t.offB;
+    a.m = t.offM >= 0 ? p.data() + t.offM : nullptr;
+    v.push_back(a);
+  }
+  return write_adapter_gguf(path, adapter_type_of(m), m.rank, m.alpha, v, err) ? 0 : 1;
+}
+
+// The adapter values of `path` into the host copy `p` of the flat parameters, with the checks of
+// train_restore_adapter_values (src/train_resume.h:104-148): same type, rank and alpha, the same
+// set of targets, every tensor of the expected size.
+static int read_adapter_file(const DitModel& m, const std::string& path, std::vector<float>& p, std::string& err) {
+  GgufFile f;
+  if (!f.open(path, err)) return 1;
+  const GgufValue* ty = f.find("lora.adapter_type");
+  const GgufValue* rk = f.find("lora.rank");
+  const GgufValue* al = f.find("lora.alpha");
+  const std::string type = ty && ty->type == kGgufString ? ty->s : "lora";
+  if (!rk || rk->type != kGgufU32 || !al || al->type != kGgufF32) {
+    err = "adapter file has no lora.rank / lora.alpha: " + path;
+    return 1;
+  }
+  if (type != adapter_type_of(m) || (int)rk->u != m.rank || (float)al->f != m.alpha) {
+    err = "adapter type/rank/alpha of " + path + " does not match the model's adapters";
+    return 1;
+  }
+  size_t stems = 0;
+  for (const std::string& n : f.tensor_order)
+    if (n.size() > 7 && n.compare(n.size() - 7, 7, ".lora_A") == 0) ++stems;
+  if (stems != m.tg.size()) {
+    err = "adapter file target count does not match the model's adapters";
+    return 1;
+  }
+  for (const DitTarget& t : m.tg) {
+    const std::string st = stem_of(t.name);
+    struct Part { const char* kind; int64_t off, count; };
+    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
+    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    for (const Part& q : parts) {
+      std::vector<float> v;
+      const std::string name = st + "." + q.kind;
+      if (!f.tensors.count(name)) {
+        err = "adapter file is missing " + name;
+        return 1;
+      }
+      if (!f.read_f32(name, v, err)) return 1;
+      if ((int64_t)v.size() != q.count) {
+        err = "adapter tensor shape mismatch: " + name;
+        return 1;
+      }
+      std::copy(v.begin(), v.end(), p.begin() + q.off);
+    }
+  }
+  return 0;
+}
+
+static bool file_exists(const std::string& p) {
+  struct stat st;
+  return stat(p.c_str(), &st) == 0;
+}
+
+static std::string base_name(const std::string& p) {
+  const size_t k = p.find_last_of('/');
+  return k == std::string::npos ? p : p.substr(k + 1);
+}
+
+int sa3k_dit_save_adapter(sa3k_dit* d, const char* path, char* err, int err_len) {
+  if (!d || !path) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters");
+  cudaSetDevice(m.c->device);
+  std::string e;
+  if (write_adapter_file(m, path, e)) return dfail(err, err_len, e);
+  return 0;
+}
+
+int sa3k_dit_load_adapter(sa3k_dit* d, const char* path, char* err, int err_len) {
+  if (!d || !path) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters: call sa3k_dit_init_adapters first");
+  cudaSetDevice(m.c->device);
+  std::string e;
+  std::vector<float> p((size_t)m.np, 0.f);
+  if (read_adapter_file(m, path, p, e) || store_flat(m, m.p, p, e)) return dfail(err, err_len, e);
+  return 0;
+}
+
+int sa3k_dit_save_checkpoint(sa3k_dit* d, const char* adapter_path, const char* state_path, int64_t step,
+                             const sa3k_train_progress* pr, char* err, int err_len) {
+  if (!d || !adapter_path || !state_path || !pr) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters");
+  if (step <= 0 || !pr->order || pr->n_order <= 0 || pr->next_sample > (uint64_t)pr->n_order)
+    return dfail(err, err_len, "cannot write invalid trainer continuation state");
+  const std::string ap(adapter_path), sp(state_path);
+  if (file_exists(ap) || file_exists(sp))
+    return dfail(err, err_len, "refusing to overwrite an existing immutable training checkpoint at step " +
+                                   std::to_string(step));
+  cudaSetDevice(m.c->device);
+  std::string e;
+  std::vector<float> mom, vel;
+  if (fetch_flat(m, m.am, mom, e) || fetch_flat(m, m.av, vel, e)) return dfail(err, err_len, e);
+  const std::string atmp = ap + ".tmp", stmp = sp + ".tmp";
+  std::remove(atmp.c_str());
+  std::remove(stmp.c_str());
+  auto cleanup = [&]() {
+    std::remove(atmp.c_str());
+    std::remove(stmp.c_str());
+  };
+  if (write_adapter_file(m, atmp, e)) {
+    cleanup();
+    return dfail(err, err_len, e);
+  }
+  const std::string fp = gguf_file_fingerprint(atmp, e);
+  if (fp.empty()) {
+    cleanup();
+    return dfail(err, err_len, e);
+  }
+  // trainer state (write_train_state_gguf, src/train_resume.h:336-381)
+  GgufWriter w;
+  auto s = [](const char* x) { return std::string(x ? x : ""); };
+  w.set_str("general.architecture", "sa3-trainer-state");
+  w.set_str("general.name", "sa3 native trainer continuation state");
+  w.set_u32("trainer.state_version", 1);
+  w.set_u64("trainer.step", (uint64_t)step);
+  w.set_u64("trainer.epoch", pr->epoch);
+  w.set_u64("trainer.next_sample", pr->next_sample);
+  w.set_u32("trainer.n_targets", (uint32_t)m.tg.size());
+  w.set_str("trainer.adapter_file", base_name(ap));
+  w.set_str("trainer.adapter_fingerprint", fp);
+  w.set_str("trainer.compatibility", s(pr->compatibility));
+  w.set_str("trainer.rng.shuffle", s(pr->rng_shuffle));
+  w.set_str("trainer.rng.crop", s(pr->rng_crop));
+  w.set_str("trainer.rng.cfg", s(pr->rng_cfg));
+  w.set_str("trainer.rng.prompt", s(pr->rng_prompt));
+  w.set_str("trainer.rng.inpaint", s(pr->rng_inpaint));
+  w.set_str("trainer.rng.diffusion", s(pr->rng_diffusion));
+  w.set_arr_u64("trainer.order", std::vector<uint64_t>(pr->order, pr->order + pr->n_order));
+  std::vector<std::string> stems;
+  for (size_t i : file_order(m)) stems.push_back(stem_of(m.tg[i].name));
+  w.set_arr_str("trainer.targets", stems);
+  for (size_t i : file_order(m)) {
+    const DitTarget& t = m.tg[i];
+    const std::string base = "optimizer." + stem_of(t.name) + ".";
+    struct Part { const char* kind; int64_t off, count; };
+    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
+    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    for (const Part& q : parts) {
+      w.add_f32(base + q.kind + ".m", {q.count}, mom.data() + q.off);
+      w.add_f32(base + q.kind + ".v", {q.count}, vel.data() + q.off);
+    }
+  }
+  if (!w.write(stmp, e)) {
+    cleanup();
+    return dfail(err, err_len, e);
+  }
+  // publish: the adapter first, the state last (its presence marks a complete pair)
+  if (std::rename(atmp.c_str(), ap.c_str()) != 0) {
+    cleanup();
+    return dfail(err, err_len, "failed to publish adapter checkpoint " + ap);
+  }
+  if (std::rename(stmp.c_str(), sp.c_str()) != 0) {
+    std::remove(stmp.c_str());
+    return dfail(err, err_len, "adapter was written, but trainer state could not be published: " + sp);
+  }
+  return 0;
+}
+
+int sa3k_dit_load_checkpoint(sa3k_dit* d, const char* adapter_path, const char* state_path, int64_t* step,
+                             char* err, int err_len) {
+  if (!d || !adapter_path || !state_path || !step) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters: call sa3k_dit_init_adapters first");
+  cudaSetDevice(m.c->device);
+  std::string e;
+  GgufFile f;
+  if (!f.open(state_path, e)) return dfail(err, err_len, e);
+  const GgufValue* arch = f.find("general.architecture");
+  if (!arch || arch->type != kGgufString || arch->s != "sa3-trainer-state")
+    return dfail(err, err_len, std::string("not an sa3 trainer-state GGUF: ") + state_path);
+  const GgufValue* ver = f.find("trainer.state_version");
+  if (!ver || ver->type != kGgufU32 || ver->u != 1) return dfail(err, err_len, "unsupported trainer-state version");
+  const GgufValue* st = f.find("trainer.step");
+  const GgufValue* fp = f.find("trainer.adapter_fingerprint");
+  if (!st || st->type != kGgufU64 || !fp || fp->type != kGgufString)
+    return dfail(err, err_len, "trainer state is missing its step or adapter fingerprint");
+  const std::string actual = gguf_file_fingerprint(adapter_path, e);
+  if (actual.empty()) return dfail(err, err_len, e);
+  if (actual != fp->s) return dfail(err, err_len, "resume adapter does not match its trainer-state sidecar");
+  const GgufValue* tg = f.find("trainer.targets");
+  std::vector<std::string> stems;
+  for (size_t i : file_order(m)) stems.push_back(stem_of(m.tg[i].name));
+  if (!tg || tg->type != kGgufArray || tg->arr_type != kGgufString || tg->arr_s != stems)
+    return dfail(err, err_len, "trainer state target inventory does not match the model's adapters");
+  std::vector<float> p((size_t)m.np, 0.f), mom((size_t)m.np, 0.f), vel((size_t)m.np, 0.f);
+  if (read_adapter_file(m, adapter_path, p, e)) return dfail(err, err_len, e);
+  for (const DitTarget& t : m.tg) {
+    const std::string base = "optimizer." + stem_of(t.name) + ".";
+    struct Part { const char* kind; int64_t off, count; };
+    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
+    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    for (const Part& q : parts) {
+      for (int k = 0; k < 2; ++k) {
+        const std::string name = base + q.kind + (k ? ".v" : ".m");
+        std::vector<float> v;
+        if (!f.tensors.count(name)) return dfail(err, err_len, "trainer state is missing optimizer tensor " + name);
+        if (!f.read_f32(name, v, e)) return dfail(err, err_len, e);
+        if ((int64_t)v.size() != q.count) return dfail(err, err_len, "trainer optimizer tensor shape mismatch: " + name);
+        std::copy(v.begin(), v.end(), (k ? vel : mom).begin() + q.off);
+      }
+    }
+  }
+  if (store_flat(m, m.p, p, e) || store_flat(m, m.am, mom, e) || store_flat(m, m.av, vel, e))
+    return dfail(err, err_len, e);
+  *step = (int64_t)st->u;
+  return 0;
 }
 
 }  // extern "C"

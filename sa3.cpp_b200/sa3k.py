@@ -26,7 +26,9 @@ ABI_SYMBOLS = (
     "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
     "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create",
     "sa3k_dp_comm_destroy", "sa3k_dp_comm_info", "sa3k_dp_allreduce_sum", "sa3k_dp_allreduce_adamw",
-    "sa3k_dit_dp_apply_adamw",
+    "sa3k_dit_dp_apply_adamw", "sa3k_dit_save_adapter", "sa3k_dit_load_adapter", "sa3k_dit_save_checkpoint",
+    "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
+    "sa3k_gguf_get_u64_array", "sa3k_gguf_get_f32",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
@@ -65,6 +67,15 @@ class DitConfigC(ctypes.Structure):
 
 class ProfileEntry(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
+
+
+class TrainProgress(ctypes.Structure):
+    """sa3k_train_progress: the dataset-side progress stored in a trainer-state file."""
+    _fields_ = [("epoch", ctypes.c_uint64), ("next_sample", ctypes.c_uint64),
+                ("order", ctypes.POINTER(ctypes.c_uint64)), ("n_order", ctypes.c_int64),
+                ("compatibility", ctypes.c_char_p), ("rng_shuffle", ctypes.c_char_p), ("rng_crop", ctypes.c_char_p),
+                ("rng_cfg", ctypes.c_char_p), ("rng_prompt", ctypes.c_char_p), ("rng_inpaint", ctypes.c_char_p),
+                ("rng_diffusion", ctypes.c_char_p)]
 
 
 class AdamWParams(ctypes.Structure):
@@ -131,6 +142,17 @@ def lib():
         L.sa3k_dit_dp_apply_adamw.argtypes = [P, P, I, ctypes.POINTER(AdamWParams), I,
                                               ctypes.POINTER(ctypes.c_double), E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
+        L.sa3k_dit_save_adapter.argtypes = [P, E, E, I]
+        L.sa3k_dit_load_adapter.argtypes = [P, E, E, I]
+        L.sa3k_dit_save_checkpoint.argtypes = [P, E, E, I64, ctypes.POINTER(TrainProgress), E, I]
+        L.sa3k_dit_load_checkpoint.argtypes = [P, E, E, ctypes.POINTER(I64), E, I]
+        PP = ctypes.POINTER(ctypes.c_void_p)
+        L.sa3k_adapter_gguf_write.argtypes = [E, E, I, F, I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I64),
+                                              ctypes.POINTER(I64), PP, PP, PP, E, I]
+        L.sa3k_gguf_get_string.argtypes = [E, E, E, I64, ctypes.POINTER(I64), E, I]
+        L.sa3k_gguf_get_u64.argtypes = [E, E, ctypes.POINTER(ctypes.c_uint64), E, I]
+        L.sa3k_gguf_get_u64_array.argtypes = [E, E, ctypes.POINTER(ctypes.c_uint64), I64, ctypes.POINTER(I64), E, I]
+        L.sa3k_gguf_get_f32.argtypes = [E, E, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
             if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free", "sa3k_dit_free",
                             "sa3k_dp_comm_destroy"):
@@ -384,6 +406,37 @@ class Dit:
         _check(lib().sa3k_dit_adapter_buffer(self._h, which, ctypes.byref(p), err, 256), err)
         return p.value
 
+    def save_adapter(self, path):
+        """The adapters as the reference's adapter GGUF (loads in its generator)."""
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_save_adapter(self._h, path.encode(), err, 512), err)
+
+    def load_adapter(self, path):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_load_adapter(self._h, path.encode(), err, 512), err)
+
+    def save_checkpoint(self, adapter_path, state_path, step, epoch=0, next_sample=0, order=(0,), compatibility="",
+                        rng=None):
+        """Immutable adapter + trainer-state pair; rng: dict of the sampler states (shuffle, crop, cfg, prompt,
+        inpaint, diffusion) as strings."""
+        rng = rng or {}
+        order_arr = (ctypes.c_uint64 * len(order))(*order)
+        pr = TrainProgress(epoch, next_sample, order_arr, len(order), compatibility.encode(),
+                           *[rng.get(k, "").encode() for k in ("shuffle", "crop", "cfg", "prompt", "inpaint",
+                                                               "diffusion")])
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_save_checkpoint(self._h, adapter_path.encode(), state_path.encode(), step,
+                                              ctypes.byref(pr), err, 512), err)
+
+    def load_checkpoint(self, adapter_path, state_path):
+        """Restores parameters and AdamW moments; returns the step (the rest of the progress is read with
+        gguf_get_*)."""
+        err = ctypes.create_string_buffer(512)
+        st = ctypes.c_int64()
+        _check(lib().sa3k_dit_load_checkpoint(self._h, adapter_path.encode(), state_path.encode(), ctypes.byref(st),
+                                              err, 512), err)
+        return st.value
+
     def zero_grads(self):
         err = ctypes.create_string_buffer(256)
         _check(lib().sa3k_dit_zero_grads(self._h, err, 256), err)
@@ -454,3 +507,61 @@ class DpComm:
             self.close()
         except Exception:
             pass
+
+
+# ------------------------------------------------------------------ GGUF adapter / trainer-state files
+def adapter_gguf_write(path, adapter_type, rank, alpha, targets):
+    """targets: list of (stem, A [rank][in], B [out][rank], m [out] or None), numpy float32."""
+    import numpy as np
+    n = len(targets)
+    arrs = [(np.ascontiguousarray(A, np.float32), np.ascontiguousarray(Bm, np.float32),
+             None if m is None else np.ascontiguousarray(m, np.float32)) for _, A, Bm, m in targets]
+    stems = (ctypes.c_char_p * n)(*[t[0].encode() for t in targets])
+    ins = (ctypes.c_int64 * n)(*[a[0].shape[1] for a in arrs])
+    outs = (ctypes.c_int64 * n)(*[a[1].shape[0] for a in arrs])
+    Ap = (ctypes.c_void_p * n)(*[a[0].ctypes.data for a in arrs])
+    Bp = (ctypes.c_void_p * n)(*[a[1].ctypes.data for a in arrs])
+    Mp = (ctypes.c_void_p * n)(*[(a[2].ctypes.data if a[2] is not None else None) for a in arrs])
+    err = ctypes.create_string_buffer(512)
+    _check(lib().sa3k_adapter_gguf_write(path.encode(), adapter_type.encode(), rank, alpha, n, stems, ins, outs, Ap,
+                                         Bp, Mp, err, 512), err)
+
+
+def gguf_get_string(path, key):
+    err = ctypes.create_string_buffer(512)
+    n = ctypes.c_int64()
+    _check(lib().sa3k_gguf_get_string(path.encode(), key.encode(), None, 0, ctypes.byref(n), err, 512), err)
+    buf = ctypes.create_string_buffer(n.value + 1)
+    _check(lib().sa3k_gguf_get_string(path.encode(), key.encode(), buf, n.value + 1, None, err, 512), err)
+    return buf.raw[:n.value].decode()
+
+
+def gguf_get_u64(path, key):
+    err = ctypes.create_string_buffer(512)
+    v = ctypes.c_uint64()
+    _check(lib().sa3k_gguf_get_u64(path.encode(), key.encode(), ctypes.byref(v), err, 512), err)
+    return v.value
+
+
+def gguf_get_u64_array(path, key):
+    err = ctypes.create_string_buffer(512)
+    n = ctypes.c_int64()
+    _check(lib().sa3k_gguf_get_u64_array(path.encode(), key.encode(), None, 0, ctypes.byref(n), err, 512), err)
+    out = (ctypes.c_uint64 * max(n.value, 1))()
+    _check(lib().sa3k_gguf_get_u64_array(path.encode(), key.encode(), out, n.value, ctypes.byref(n), err, 512), err)
+    return list(out[:n.value])
+
+
+def gguf_get_f32(path, name):
+    """(values as a flat numpy float32 array, ne tuple with ne[0] innermost)."""
+    import numpy as np
+    err = ctypes.create_string_buffer(512)
+    n = ctypes.c_int64()
+    ne = (ctypes.c_int64 * 4)()
+    nd = ctypes.c_int()
+    _check(lib().sa3k_gguf_get_f32(path.encode(), name.encode(), None, 0, ctypes.byref(n), ne, ctypes.byref(nd), err,
+                                   512), err)
+    out = np.empty(n.value, np.float32)
+    _check(lib().sa3k_gguf_get_f32(path.encode(), name.encode(), out.ctypes.data_as(ctypes.c_void_p), n.value,
+                                   ctypes.byref(n), ne, ctypes.byref(nd), err, 512), err)
+    return out, tuple(ne[:nd.value])
