@@ -140,6 +140,32 @@ typedef struct sa3k_adapter {
 int sa3k_linear_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad,
                     const float* bias, const float* x, int64_t S, float* y, char* err, int err_len);
 
+/* ---- inference with a chain of functional adapters (build_functional_lora, src/lora.h:372-622,
+ * and the DitLoraParam::terms path of dit_lin, src/dit.h:108-117) ----
+ * One adapter of a chain, in chain order: A [rank][in], B [out][rank], magnitude [out] for
+ * dora-rows (NULL for lora), scale = alpha / rank * strength.  Device pointers, read at build. */
+typedef struct sa3k_chain_term {
+  const float* A;
+  const float* B;
+  const float* magnitude;
+  int rank;
+  float scale;
+} sa3k_chain_term;
+typedef struct sa3k_lora_chain sa3k_lora_chain;
+/* Folds the chain for weight w on the device: every dora-rows adapter rescales the rows of the
+ * weight accumulated before it (base row norms, W A^T and A A^T terms; no materialized weight).
+ * 1..16 adapters, at most 64 ranks in all.  The chain keeps its own device memory. */
+int sa3k_lora_chain_build(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_chain_term* terms, int n,
+                          sa3k_lora_chain** out, char* err, int err_len);
+void sa3k_lora_chain_free(sa3k_lora_chain* chain);
+/* total rank of the chain and whether its forward is one fused GEMM (rank <= 16 and no output row
+ * whose base scale is 0); returns 0 */
+int sa3k_lora_chain_info(const sa3k_lora_chain* chain, int* total_rank, int* fused);
+/* y[S][out] = b * (x W^T) + sum_k scale_k (x A_k^T) B'_k^T + bias for the chain's weight (x, y,
+ * bias f32 device). */
+int sa3k_linear_fwd_chain(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_lora_chain* chain,
+                          const float* bias, const float* x, int64_t S, float* y, char* err, int err_len);
+
 /* Backward of sa3k_linear_fwd for upstream dy[S][out], given its inputs x and its output y.
  * Writes dx[S][in] (if non-NULL) and the adapter gradients dA[rank][in], dB[out][rank],
  * dm[out] (dora; each may be NULL when ad is NULL).  accumulate != 0 adds into dx/dA/dB/dm

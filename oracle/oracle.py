@@ -25,6 +25,8 @@ the reference's math for the path:
   AdamW              src/train_optimizer.h:42-65 (the reference's own compiled code is
                      oracle/_ref/libsa3ref.so; adamw_f32 below restates it)
   expo_features      src/sa3_pipeline.h:57-67
+  functional chain   src/lora.h:372-622 (build_functional_lora: base scale and row-scaled B' of a
+                     chain of lora / dora-rows adapters) + src/dit.h:108-117 (its dit_lin terms)
 
 Layout convention: ggml [ne0, ne1] is row-major [ne1][ne0].  So W [in,out] is W[out][in]
 (quant blocks run along `in`), x [in,S] is x[S][in], A [in,r] is A[r][in], B [r,out] is B[out][r].
@@ -229,6 +231,66 @@ def effective_weight(W, A, B, scale, m=None):
     # rms_norm(v, 1e-12) / sqrt(in) == v / sqrt(sum v^2 + in*1e-12)
     nrm = np.sqrt((v * v).sum(1) + inn * 1e-12)
     return v / nrm[:, None] * np.asarray(m, np.float64)[:, None]
+
+
+def functional_chain(W, terms, bns=None):
+    """build_functional_lora (src/lora.h:372-622) for one target, in float64.  terms: list of
+    (A [r][in], B [out][r], m [out] or None, s) in chain order (s = alpha / rank * strength).
+    Returns (b [out] or None, [g_k [out]]): the base scale and each residual's row coefficient,
+    walked as the reference does (:531-554) from the low-rank quantities nsq0 = |W|^2 + in eps,
+    T2_k = rowdot(W A_k^T, B_k) and G_kl = rowdot(B_k (A_k A_l^T), B_l)."""
+    W = np.asarray(W, np.float64)
+    out, inn = W.shape
+    nsq0 = (W * W).sum(1) + inn * 1e-12 if bns is None else np.asarray(bns, np.float64)
+    A = [np.asarray(t[0], np.float64) for t in terms]
+    B = [np.asarray(t[1], np.float64) for t in terms]
+    n = len(terms)
+    T2 = [((W @ A[k].T) * B[k]).sum(1) for k in range(n)]
+    G = [[((B[k] @ (A[k] @ A[l].T)) * B[l]).sum(1) for l in range(n)] for k in range(n)]
+    b = None
+    g = [None] * n
+    one = lambda v: 1.0 if v is None else v
+    for j in range(n):
+        if terms[j][2] is None:
+            continue
+        nsq = nsq0 * (one(b) ** 2)
+        for k in range(j + 1):
+            nsq = nsq + T2[k] * one(g[k]) * 2.0 * terms[k][3] * one(b)
+        for k in range(j + 1):
+            for l in range(k, j + 1):
+                nsq = nsq + G[k][l] * one(g[k]) * one(g[l]) * terms[k][3] * terms[l][3] * (1.0 if k == l else 2.0)
+        d = np.asarray(terms[j][2], np.float64) / np.sqrt(nsq)
+        b = d if b is None else b * d
+        for k in range(j + 1):
+            g[k] = d if g[k] is None else g[k] * d
+    return b, [np.ones(out) if x is None else x for x in g]
+
+
+def functional_chain_forward(x, W, terms, bias=None):
+    """dit_lin with a term chain (src/dit.h:108-117): y = b (x W^T) + sum_k s_k (x A_k^T) (g_k B_k)^T + bias."""
+    x = np.asarray(x, np.float64)
+    b, g = functional_chain(W, terms)
+    y = x @ np.asarray(W, np.float64).T
+    if b is not None:
+        y = y * b
+    for k, (A, B, m, s) in enumerate(terms):
+        y = y + s * (x @ np.asarray(A, np.float64).T) @ (g[k][:, None] * np.asarray(B, np.float64)).T
+    if bias is not None:
+        y = y + bias
+    return y
+
+
+def chain_weight(W, terms):
+    """The chain by its definition: adapters applied in order to the materialized weight, each
+    lora adding s B A, each dora-rows rescaling every row of the sum to its magnitude
+    (merge order of the reference's adapter chain)."""
+    V = np.asarray(W, np.float64)
+    inn = V.shape[1]
+    for A, B, m, s in terms:
+        V = V + s * (np.asarray(B, np.float64) @ np.asarray(A, np.float64))
+        if m is not None:
+            V = V / np.sqrt((V * V).sum(1) + inn * 1e-12)[:, None] * np.asarray(m, np.float64)[:, None]
+    return V
 
 
 # --------------------------------------------------------------------------------------------

@@ -126,7 +126,8 @@ inline int check_launch(const char* what, std::string& err) {
 }
 
 // Scratch slots owned by a context (see api.cu for the linear path's slots).
-enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61, kSlotSplitCnt = 60 };
+enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61, kSlotSplitCnt = 60, kSlotChainX = 59,
+             kSlotChainU = 58 };
 
 // Scratch slot `slot` of at least `bytes` (grows; contents are not preserved on growth).
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);

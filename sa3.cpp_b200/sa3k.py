@@ -28,7 +28,8 @@ ABI_SYMBOLS = (
     "sa3k_dp_comm_destroy", "sa3k_dp_comm_info", "sa3k_dp_allreduce_sum", "sa3k_dp_allreduce_adamw",
     "sa3k_dit_dp_apply_adamw", "sa3k_dit_save_adapter", "sa3k_dit_load_adapter", "sa3k_dit_save_checkpoint",
     "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
-    "sa3k_gguf_get_u64_array", "sa3k_gguf_get_f32",
+    "sa3k_gguf_get_u64_array", "sa3k_gguf_get_f32", "sa3k_lora_chain_build", "sa3k_lora_chain_free",
+    "sa3k_lora_chain_info", "sa3k_linear_fwd_chain",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
@@ -67,6 +68,12 @@ class DitConfigC(ctypes.Structure):
 
 class ProfileEntry(ctypes.Structure):
     _fields_ = [("name", ctypes.c_char * 48), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double)]
+
+
+class ChainTerm(ctypes.Structure):
+    """sa3k_chain_term: one adapter of an inference chain (device pointers)."""
+    _fields_ = [("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("magnitude", ctypes.c_void_p), ("rank", ctypes.c_int),
+                ("scale", ctypes.c_float)]
 
 
 class TrainProgress(ctypes.Structure):
@@ -142,6 +149,11 @@ def lib():
         L.sa3k_dit_dp_apply_adamw.argtypes = [P, P, I, ctypes.POINTER(AdamWParams), I,
                                               ctypes.POINTER(ctypes.c_double), E, I]
         L.sa3k_profile_read.argtypes = [P, ctypes.POINTER(ProfileEntry), I, ctypes.POINTER(I), E, I]
+        L.sa3k_lora_chain_build.argtypes = [P, P, ctypes.POINTER(ChainTerm), I, ctypes.POINTER(P), E, I]
+        L.sa3k_lora_chain_free.argtypes = [P]
+        L.sa3k_lora_chain_free.restype = None
+        L.sa3k_lora_chain_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
+        L.sa3k_linear_fwd_chain.argtypes = [P, P, P, P, P, I64, P, E, I]
         L.sa3k_dit_save_adapter.argtypes = [P, E, E, I]
         L.sa3k_dit_load_adapter.argtypes = [P, E, E, I]
         L.sa3k_dit_save_checkpoint.argtypes = [P, E, E, I64, ctypes.POINTER(TrainProgress), E, I]
@@ -155,7 +167,7 @@ def lib():
         L.sa3k_gguf_get_f32.argtypes = [E, E, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I), E, I]
         for name in ABI_SYMBOLS:
             if name not in ("sa3k_version", "sa3k_ctx_destroy", "sa3k_weight_free", "sa3k_dit_free",
-                            "sa3k_dp_comm_destroy"):
+                            "sa3k_dp_comm_destroy", "sa3k_lora_chain_free"):
                 getattr(L, name).restype = I
         L.sa3k_dit_adapter_size.restype = I64
         _lib = L
@@ -297,6 +309,21 @@ class Context:
         _check(lib().sa3k_linear_fwd(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias), _ptr(x),
                                      x.shape[0], _ptr(y), err, 512), err)
 
+    def lora_chain(self, w, terms):
+        """terms: list of (A [rank][in], B [out][rank], magnitude [out] or None, scale) torch cuda f32 tensors,
+        in chain order.  Returns a LoraChain (folded on the device)."""
+        arr = (ChainTerm * len(terms))(*[ChainTerm(A.data_ptr(), B.data_ptr(), m.data_ptr() if m is not None else None,
+                                                   A.shape[0], s) for A, B, m, s in terms])
+        h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_lora_chain_build(self._h, w._h, arr, len(terms), ctypes.byref(h), err, 512), err)
+        return LoraChain(h)
+
+    def linear_fwd_chain(self, w, chain, x, y, bias=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_fwd_chain(self._h, w._h, chain._h, _ptr(bias), _ptr(x), x.shape[0], _ptr(y), err,
+                                           512), err)
+
     def linear_bwd(self, w, x, y, dy, dx, ad=None, bias=None, dA=None, dB=None, dm=None, accumulate=False):
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_linear_bwd(self._h, w._h, ctypes.byref(ad) if ad else None, _ptr(bias), _ptr(x),
@@ -341,6 +368,27 @@ class Weight:
             self._h = ctypes.c_void_p()
 
     close = free
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class LoraChain:
+    def __init__(self, h):
+        self._h = h
+
+    def info(self):
+        r, f = ctypes.c_int(), ctypes.c_int()
+        lib().sa3k_lora_chain_info(self._h, ctypes.byref(r), ctypes.byref(f))
+        return r.value, bool(f.value)
+
+    def free(self):
+        if self._h:
+            lib().sa3k_lora_chain_free(self._h)
+            self._h = ctypes.c_void_p()
 
     def __del__(self):
         try:
