@@ -283,6 +283,11 @@ int sa3k_average_clip_adamw(sa3k_ctx* ctx, float* p, const float* g, float* m, f
 typedef struct sa3k_dit_config {
   int io, dim, depth, heads, head_dim, cond_dim, mem_tokens, rot, time_dim, ff_inner, differential;
   float rope_base, norm_eps, qk_eps, time_min_freq, time_max_freq;
+  /* inpaint local-conditioning width (dit.local_dim, src/dit.h:29-30; 0: none).  The per-block
+   * dit.N.local.{0,2} tensors then load, and adapters on them are carried (saved, updated by
+   * AdamW) with zero gradients: the training step takes no local-conditioning input, as the
+   * reference's step without an inpaint input (src/dit.h:246). */
+  int local_dim;
 } sa3k_dit_config;
 
 typedef struct sa3k_dit sa3k_dit;

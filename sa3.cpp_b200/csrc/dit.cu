@@ -51,6 +51,11 @@ struct DitTarget {
   // the grouped adapter-gradient pass (activation arena): dz [rows][out] bf16, dg [out], du^T
   // [16][ut_ld] bf16, cb [16][out] bf16 (dora), c3 [16][16]; and the forward's input rows x_bf
   int64_t rows = 0, ut_ld = 0;
+  // inert: an adapter on a weight the step never computes with (the inpaint local.* projections
+  // without a local-conditioning input): carried with zero gradients, left out of every
+  // per-step adapter kernel; act = the index among the other (active) targets
+  bool inert = false;
+  int act = -1;
   __nv_bfloat16 *ut = nullptr, *dz = nullptr, *dut = nullptr, *cb = nullptr;
   float *dg = nullptr, *c3 = nullptr;
   const __nv_bfloat16* x_bf = nullptr;
@@ -80,6 +85,10 @@ struct DitModel {
   std::map<std::string, Weight*> W;
   std::vector<sa3k_weight*> weights;   // owned weight handles (W points into them)
   std::map<std::string, float*> V;
+  // weights kept on the host only: inpaint local.* projections whose `in` the GEMM engine does
+  // not tile (dit.local_dim = 257); [out][in] f32 with their (in, out)
+  std::map<std::string, std::vector<float>> host_w;
+  std::map<std::string, std::pair<int64_t, int64_t>> host_shape;
   std::vector<void*> owned;            // device allocations of this model
   // adapters
   bool dora = false;
@@ -90,7 +99,8 @@ struct DitModel {
   float *p = nullptr, *g = nullptr, *am = nullptr, *av = nullptr;
   int64_t np = 0;
   void* prep_mem = nullptr;
-  PrepDesc* prep_desc = nullptr;       // device descriptors of the adapters (grouped preparation)
+  PrepDesc* prep_desc = nullptr;       // device descriptors of the active adapters (grouped preparation)
+  int n_active = 0;
   int64_t max_out = 0;
   // grouped rank-16 GEMMs: DoRA P = W A^T of every adapter (forward preparation) and every
   // adapter's dB / dA contractions (end of the backward); bound to the activation arena
@@ -237,6 +247,7 @@ static bool has_target(const DitModel& m, const char* fragment) {
 
 static int bind_adapter_grads(DitModel& m, std::string& err) {
   for (DitTarget& t : m.tg) {
+    if (t.inert) continue;
     t.x_bf = target_input(m, t.name);
     if (!t.x_bf) {
       err = "adapter target " + t.name + " is not a linear of the DiT";
@@ -246,6 +257,7 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
   std::vector<PrepDesc> descs;
   std::vector<R16Job> prep, grads;
   for (DitTarget& t : m.tg) {
+    if (t.inert) continue;
     const AdapterPrep& p = t.prep;
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
@@ -284,18 +296,19 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
       prep.push_back(j);
     }
   }
-  if (cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+  if (!descs.empty() &&
+      cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
     err = "adapter descriptor upload failed";
     return 1;
   }
   // every DoRA base needs its bf16 copy for the grouped P and dA terms (else the per-adapter
   // GEMMs over the quantized codes run instead)
   bool all_bf16 = true;
-  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (!t.prep.dora() || t.w->bf16);
+  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (t.inert || !t.prep.dora() || t.w->bf16);
   r16_group_free(m.r16_prep);
   r16_group_free(m.r16_grads);
-  if (!all_bf16) return 0;
-  if (r16_group_build(m.c, prep, 24, m.r16_prep, err)) return 1;
+  if (!all_bf16 || grads.empty()) return 0;
+  if (!prep.empty() && r16_group_build(m.c, prep, 24, m.r16_prep, err)) return 1;
   return r16_group_build(m.c, grads, 24, m.r16_grads, err);
 }
 
@@ -370,15 +383,16 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     const int64_t maxout = std::max<int64_t>(wide, 6 * D);
     m.dg = f(maxout); m.c3 = f(256);
     m.dut = h(16 * m.ut_ld); m.dz = h(Mx * maxout); m.cb = h(16 * maxout);
-    m.c3_all = f(256 * (int64_t)m.tg.size());
+    m.c3_all = f(256 * (int64_t)std::max(m.n_active, 1));
     for (size_t i = 0; i < m.tg.size(); ++i) {
       DitTarget& t = m.tg[i];
+      if (t.inert) continue;
       t.rows = target_rows(m, t.name);
       t.ut_ld = (t.rows + 63) / 64 * 64;
       t.ut = h(16 * t.ut_ld);
       t.dz = h(t.rows * t.out); t.dg = f(t.out); t.dut = h(16 * t.ut_ld);
       t.cb = m.dora ? h(16 * t.out) : nullptr;
-      t.c3 = m.c3_all ? m.c3_all + 256 * (int64_t)i : nullptr;
+      t.c3 = m.c3_all ? m.c3_all + 256 * (int64_t)t.act : nullptr;
     }
     if (pass == 0) {
       m.arena_bytes = off;
@@ -514,15 +528,15 @@ static int dit_step(DitModel& m, std::string& err) {
 
   // adapters: operand forms + DoRA norms, once per step (grouped launches over all adapters; the
   // DoRA P = W A^T GEMMs run per adapter between them)
-  const int nt = (int)m.tg.size();
-  if (k_prep_all(c, m.prep_desc, nt, err)) return 1;
-  if (m.dora) {
+  const int nt = m.n_active;
+  if (nt > 0 && k_prep_all(c, m.prep_desc, nt, err)) return 1;
+  if (m.dora && nt > 0) {
     if (k_aat_all(c, m.prep_desc, nt, err)) return 1;
     if (m.r16_prep.table) {
       if (r16_group_run(c, m.r16_prep, "dora.P", err)) return 1;
     } else {
       for (DitTarget& t : m.tg)
-        if (adapter_dora_p(c, t.w, t.prep, err)) return 1;
+        if (!t.inert && adapter_dora_p(c, t.w, t.prep, err)) return 1;
     }
     if (k_dora_norm_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
   }
@@ -839,7 +853,7 @@ static int dit_step(DitModel& m, std::string& err) {
   // dA += du^T x and dA += cb W contractions, then dA += 2 c3 A
   if (m.r16_grads.table) {
     if (m.dora) {
-      if (cudaMemsetAsync(m.c3_all, 0, sizeof(float) * 256 * m.tg.size(), c->stream) != cudaSuccess)
+      if (cudaMemsetAsync(m.c3_all, 0, sizeof(float) * 256 * std::max(m.n_active, 1), c->stream) != cudaSuccess)
         return check_launch("memset", err);
       if (k_dora_bwd_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
     }
@@ -958,6 +972,11 @@ static bool dit_tensor_shape(const sa3k_dit_config& k, const std::string& n, int
     if (b == "ff.proj.weight") return set(D, 2 * I);
     if (b == "ff.proj.bias") return set(2 * I, 1);
     if (b == "ff.out.weight") return set(I, D);
+    if (k.local_dim > 0) {
+      if (b == "local.0.weight") return set(k.local_dim, D);
+      if (b == "local.2.weight") return set(D, D);
+      if (b == "local.0.bias" || b == "local.2.bias") return set(D, 1);
+    }
     return false;
   }
   if (r == "time_embed.0.weight") return set(td, D);
@@ -1024,6 +1043,22 @@ int sa3k_dit_set_tensor(sa3k_dit* d, const char* name, int type, const void* hos
                                    std::to_string(x1) + "][" + std::to_string(x0) + "]");
   const bool is_weight = n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0;
   std::string e;
+  if (is_weight && ne0 % 64 != 0) {
+    // kept on the host (only the inpaint local.0 projection has such a width here)
+    if (m.host_w.count(n)) return dfail(err, err_len, "tensor set twice: " + n);
+    if (type != SA3K_TYPE_F32 && type != SA3K_TYPE_F16)
+      return dfail(err, err_len, n + ": a weight whose width is not a multiple of 64 must be F32 or F16");
+    std::vector<float> v((size_t)(ne0 * ne1));
+    if (type == SA3K_TYPE_F32) {
+      std::memcpy(v.data(), host, v.size() * 4);
+    } else {
+      const __half* hh = static_cast<const __half*>(host);
+      for (size_t i = 0; i < v.size(); ++i) v[i] = __half2float(hh[i]);
+    }
+    m.host_w[n] = std::move(v);
+    m.host_shape[n] = {ne0, ne1};
+    return 0;
+  }
   if (is_weight) {
     if (m.W.count(n)) return dfail(err, err_len, "tensor set twice: " + n);
     // the public upload path repacks the GGUF blocks; the model owns the handle afterwards
@@ -1062,10 +1097,20 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     DitTarget t;
     t.name = names[i];
     auto it = m.W.find(t.name);
-    if (it == m.W.end()) return dfail(err, err_len, "adapter target has no weight: " + t.name);
-    t.w = it->second;
-    t.in = t.w->in;
-    t.out = t.w->out;
+    auto ht = m.host_shape.find(t.name);
+    if (it == m.W.end() && ht == m.host_shape.end())
+      return dfail(err, err_len, "adapter target has no weight: " + t.name);
+    t.inert = t.name.find(".local.") != std::string::npos;
+    if (it != m.W.end()) {
+      t.w = it->second;
+      t.in = t.w->in;
+      t.out = t.w->out;
+    } else {
+      t.in = ht->second.first;
+      t.out = ht->second.second;
+    }
+    if (!t.inert && !t.w) return dfail(err, err_len, "adapter target has no device weight: " + t.name);
+    if (!t.inert) t.act = m.n_active++;
     t.offA = off; off += (int64_t)rank * t.in;
     t.offB = off; off += t.out * rank;
     if (m.dora) { t.offM = off; off += t.out; }
@@ -1078,8 +1123,9 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     if (!*b) return dfail(err, err_len, e);
     cudaMemsetAsync(*b, 0, (size_t)off * 4, m.c->stream);
   }
-  size_t prep_bytes = 0;
-  for (DitTarget& t : m.tg) prep_bytes += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
+  size_t prep_bytes = 256;
+  for (DitTarget& t : m.tg)
+    if (!t.inert) prep_bytes += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
   char* pm = static_cast<char*>(dmalloc(m, prep_bytes, e));
   if (!pm) return dfail(err, err_len, e);
   for (DitTarget& t : m.tg) {
@@ -1093,14 +1139,30 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
       p.bns = t.bns;
       // base_norm_sq and the magnitude init = row norms of the dequantized base
       // (train_row_norm_sq / train_row_norms, src/train_lora.h:141-174,262-263)
-      if (weight_row_norms(m.c, t.w, 1e-12f, t.bns, m.p + t.offM, e)) return dfail(err, err_len, e);
+      if (t.w) {
+        if (weight_row_norms(m.c, t.w, 1e-12f, t.bns, m.p + t.offM, e)) return dfail(err, err_len, e);
+      } else {   // a host-only weight: the same f64 sums on the host
+        const std::vector<float>& hw = m.host_w[t.name];
+        std::vector<float> nsq((size_t)t.out), nrm((size_t)t.out);
+        for (int64_t o = 0; o < t.out; ++o) {
+          double acc = 0.0;
+          for (int64_t i = 0; i < t.in; ++i) acc += (double)hw[(size_t)(o * t.in + i)] * hw[(size_t)(o * t.in + i)];
+          nsq[(size_t)o] = (float)(acc + (double)t.in * 1e-12);
+          nrm[(size_t)o] = (float)std::sqrt(acc);
+        }
+        if (cudaMemcpy(t.bns, nsq.data(), 4 * nsq.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m.p + t.offM, nrm.data(), 4 * nrm.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+          return dfail(err, err_len, "magnitude init copy failed");
+      }
     }
+    if (t.inert) continue;
     adapter_bind(p, pm);
     pm += adapter_prep_bytes(t.in, t.out, m.dora) + 256;
   }
-  // device descriptors of all adapters for the grouped preparation kernels of every step
+  // device descriptors of the active adapters for the grouped preparation kernels of every step
   std::vector<PrepDesc> descs;
   for (DitTarget& t : m.tg) {
+    if (t.inert) continue;
     const AdapterPrep& p = t.prep;
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
@@ -1110,9 +1172,10 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     descs.push_back(pd);
     m.max_out = std::max(m.max_out, p.out);
   }
-  m.prep_desc = static_cast<PrepDesc*>(dmalloc(m, sizeof(PrepDesc) * descs.size(), e));
+  m.prep_desc = static_cast<PrepDesc*>(dmalloc(m, sizeof(PrepDesc) * std::max<size_t>(descs.size(), 1), e));
   if (!m.prep_desc) return dfail(err, err_len, e);
-  if (cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+  if (!descs.empty() &&
+      cudaMemcpy(m.prep_desc, descs.data(), sizeof(PrepDesc) * descs.size(), cudaMemcpyHostToDevice) != cudaSuccess)
     return dfail(err, err_len, "adapter descriptor upload failed");
   if (cudaStreamSynchronize(m.c->stream) != cudaSuccess) return dfail(err, err_len, "adapter init failed");
   return 0;

@@ -39,6 +39,9 @@ def tensor_shapes(cfg):
             p + "ff.proj.weight": (2 * I, D), p + "ff.proj.bias": (2 * I,),
             p + "ff.out.weight": (D, I), p + "ff.out.bias": (D,),
         })
+        if cfg.get("local_dim", 0):   # inpaint local conditioning (src/dit.h:246-254)
+            s.update({p + "local.0.weight": (D, cfg["local_dim"]), p + "local.0.bias": (D,),
+                      p + "local.2.weight": (D, D), p + "local.2.bias": (D,)})
     return s
 
 

@@ -63,7 +63,8 @@ DIT_FLOAT_FIELDS = ("rope_base", "norm_eps", "qk_eps", "time_min_freq", "time_ma
 
 
 class DitConfigC(ctypes.Structure):
-    _fields_ = [(n, ctypes.c_int) for n in DIT_INT_FIELDS] + [(n, ctypes.c_float) for n in DIT_FLOAT_FIELDS]
+    _fields_ = ([(n, ctypes.c_int) for n in DIT_INT_FIELDS] + [(n, ctypes.c_float) for n in DIT_FLOAT_FIELDS] +
+                [("local_dim", ctypes.c_int)])
 
 
 class ProfileEntry(ctypes.Structure):
@@ -402,7 +403,7 @@ class Dit:
 
     def __init__(self, ctx, cfg):
         self.ctx = ctx
-        c = DitConfigC(**{k: cfg[k] for k in DIT_INT_FIELDS + DIT_FLOAT_FIELDS})
+        c = DitConfigC(**{k: cfg[k] for k in DIT_INT_FIELDS + DIT_FLOAT_FIELDS}, local_dim=cfg.get("local_dim", 0))
         self._h = ctypes.c_void_p()
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_dit_create(ctx._h, ctypes.byref(c), ctypes.byref(self._h), err, 512), err)
