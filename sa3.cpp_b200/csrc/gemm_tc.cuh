@@ -165,29 +165,45 @@ struct GemmSmem {
 // ------------------------------------------------------------------ dequantization stages
 // NT threads of the dequant warps each write BN*8/NT 16-byte chunks (8 bf16) of the B stage.
 
+// Codes to f32 without the int-to-float conversion unit (a quarter-rate pipe): a byte c placed in
+// the low mantissa byte of 2^23 (bits 0x4B0000cc, one byte permute) is the float 2^23 + c
+// exactly, and subtracting the bias recovers the code exactly, so the products below round once,
+// like the f32 multiply of the reference dequantization.
+__device__ __forceinline__ float magic_code(uint32_t w, int b) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u + (uint32_t)b));
+}
+
+// 8 int8 codes (two words) times the block scale s: the signed codes are biased by 128 (an xor of
+// the sign bits) so that each byte is 0 .. 255, then 2^23 + 128 is subtracted.
 __device__ __forceinline__ uint4 q8_chunk(uint2 q, float s) {
-  uint4 o;
-  const int8_t* qb = reinterpret_cast<const int8_t*>(&q);
-  o.x = pack_bf16x2((float)qb[0] * s, (float)qb[1] * s);
-  o.y = pack_bf16x2((float)qb[2] * s, (float)qb[3] * s);
-  o.z = pack_bf16x2((float)qb[4] * s, (float)qb[5] * s);
-  o.w = pack_bf16x2((float)qb[6] * s, (float)qb[7] * s);
-  return o;
+  const uint32_t w[2] = {q.x ^ 0x80808080u, q.y ^ 0x80808080u};
+  const uint64_t bias = f2(-8388736.0f, -8388736.0f), sc = f2(s, s);
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t ww = w[k >> 1];
+    const int b = 2 * (k & 1);
+    float lo, hi;
+    f2split(fmul2(fadd2(f2(magic_code(ww, b), magic_code(ww, b + 1)), bias), sc), lo, hi);
+    o[k] = pack_bf16x2(lo, hi);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __device__ __forceinline__ uint4 q4_chunk(uint32_t nib, float d, float m) {
   // nib holds 8 codes, element 2b in the low nibble of byte b, 2b+1 in the high nibble;
   // d*q is exact in f32 (<= 21 significant bits), so the FMA below rounds exactly like ggml's
   // separate multiply and subtract.
-  uint4 o;
-  float v[8];
+  const uint32_t lo4 = nib & 0x0F0F0F0Fu, hi4 = (nib >> 4) & 0x0F0F0F0Fu;
+  const uint64_t bias = f2(-8388608.0f, -8388608.0f), dd = f2(d, d), mm = f2(-m, -m);
+  uint32_t o[4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) v[e] = d * (float)((nib >> (4 * e)) & 0xFu) - m;
-  o.x = pack_bf16x2(v[0], v[1]);
-  o.y = pack_bf16x2(v[2], v[3]);
-  o.z = pack_bf16x2(v[4], v[5]);
-  o.w = pack_bf16x2(v[6], v[7]);
-  return o;
+  for (int b = 0; b < 4; ++b) {   // elements 2b (low nibble) and 2b + 1 (high nibble)
+    float v0, v1;
+    f2split(ffma2(dd, fadd2(f2(magic_code(lo4, b), magic_code(hi4, b)), bias), mm), v0, v1);
+    o[b] = pack_bf16x2(v0, v1);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // K-major destination chunk (row r, 16-byte column chunk c) of a [rows][64] 128B-swizzled tile.
