@@ -166,6 +166,51 @@ int sa3k_lora_chain_info(const sa3k_lora_chain* chain, int* total_rank, int* fus
 int sa3k_linear_fwd_chain(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_lora_chain* chain,
                           const float* bias, const float* x, int64_t S, float* y, char* err, int err_len);
 
+/* A materialized adapter (src/train_lora.h:24-41, 275-329): the trainer's path for dora-cols,
+ * bora and every "-xs" family (src/train_dit.h:90-164), available for lora / dora-rows too.
+ *   V = W + scale * B A            (standard families; A [rank][in], B [out][rank])
+ *   V = W + scale * U M V_xs^T     (-xs; U [out][rank], V_xs [in][rank] frozen, M [rank][rank])
+ *   lora: W_eff = V;  dora-rows: m[out] * V / |V|_row;  dora-cols: m[in] * V / |V|_col;
+ *   bora: m_c[in] * R / |R|_col with R = m_r[out] * V / |V|_row
+ * (|v| = sqrt(sum v^2 + n * 1e-12) over the n values of a row or column).  rank 1..16; every
+ * array f32 device memory, A 16-byte aligned. */
+typedef struct sa3k_mat_adapter {
+  const char* adapter_type;   /* "lora", "dora-rows", "dora-cols", "bora", each optionally "-xs" */
+  int rank;
+  float scale;                /* alpha / rank */
+  const float* A;             /* [rank][in]   (standard) */
+  const float* B;             /* [out][rank]  (standard) */
+  const float* U;             /* [out][rank]  (-xs) */
+  const float* V;             /* [in][rank]   (-xs) */
+  const float* M;             /* [rank][rank] (-xs, trainable) */
+  const float* m;             /* dora-rows [out] / dora-cols [in] */
+  const float* m_r;           /* bora [out] */
+  const float* m_c;           /* bora [in] */
+} sa3k_mat_adapter;
+
+/* Gradients written (not accumulated) by sa3k_linear_mat_fwd_bwd: dA, dB (standard) or dM
+ * (-xs), dm (dora-rows, dora-cols) or dm_r, dm_c (bora); the others may be NULL. */
+typedef struct sa3k_mat_grads {
+  float* dA;
+  float* dB;
+  float* dM;
+  float* dm;
+  float* dm_r;
+  float* dm_c;
+} sa3k_mat_grads;
+
+/* W_eff [out][in] f32 (train_lora_effective_weight, src/train_lora.h:299-329). */
+int sa3k_mat_effective_weight(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, float* weff,
+                              char* err, int err_len);
+/* y[S][out] = x W_eff^T + bias (bias may be NULL): the dit_lin of an overridden weight. */
+int sa3k_linear_mat_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, const float* bias,
+                        const float* x, int64_t S, float* y, char* err, int err_len);
+/* The forward (y may be NULL) and the backward for upstream dy[S][out]: dx[S][in] (may be NULL)
+ * and the adapter gradients (what ggml_build_backward_expand derives for the override graph). */
+int sa3k_linear_mat_fwd_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, const float* bias,
+                            const float* x, const float* dy, int64_t S, float* y, float* dx,
+                            const sa3k_mat_grads* g, char* err, int err_len);
+
 /* Backward of sa3k_linear_fwd for upstream dy[S][out], given its inputs x and its output y.
  * Writes dx[S][in] (if non-NULL) and the adapter gradients dA[rank][in], dB[out][rank],
  * dm[out] (dora; each may be NULL when ad is NULL).  accumulate != 0 adds into dx/dA/dB/dm

@@ -13,6 +13,11 @@ the reference's math for the path:
                      of src/dit.h:106-147, written out by hand (pinned by finite differences,
                      as tests/dit_lin_functional_test.cpp:132-260 does)
   W_eff              src/train_lora.h:301-329 (materialized effective weight, dora-rows)
+  materialized       src/train_lora.h:275-329 (every family: lora, dora-rows, dora-cols, bora,
+  families           and their -xs forms, delta = U M V^T) + src/train_dit.h:96-164 (which
+                     families take the materialized path); the backward is written out by hand
+                     and checked against torch autograd of the definition and against the
+                     known answers of tests/train_lora_test.cpp:130-223
   row norms          src/train_lora.h:141-174
   rms_norm           src/nn.h:40-42
   rope_neox          src/nn.h:53-59 (partial NeoX rotation of the first n_dims of each head)
@@ -231,6 +236,113 @@ def effective_weight(W, A, B, scale, m=None):
     # rms_norm(v, 1e-12) / sqrt(in) == v / sqrt(sum v^2 + in*1e-12)
     nrm = np.sqrt((v * v).sum(1) + inn * 1e-12)
     return v / nrm[:, None] * np.asarray(m, np.float64)[:, None]
+
+
+MAT_FAMILIES = ("lora", "dora-rows", "dora-cols", "bora")
+MAT_EPS = 1e-12
+
+
+def split_adapter_type(adapter_type):
+    """("bora", True) for "bora-xs" (src/train_lora.h:309-310)."""
+    xs = adapter_type.endswith("-xs")
+    fam = adapter_type[:-3] if xs else adapter_type
+    if fam not in MAT_FAMILIES:
+        raise ValueError(f"unknown adapter type {adapter_type}")
+    return fam, xs
+
+
+def mat_delta(p, xs):
+    """Low-rank update [out][in] (train_lora_delta, src/train_lora.h:290-297): B A, or for the -xs
+    forms U M V^T with U [out][r], M [r][r] (M[a][b] = M_xs data[a*r+b]), V [in][r]."""
+    f = lambda k: np.asarray(p[k], np.float64)
+    if xs:
+        return f("U") @ f("M") @ f("V").T
+    return f("B") @ f("A")
+
+
+def mat_effective_weight(W, p, adapter_type, scale):
+    """W_eff [out][in] of any family (src/train_lora.h:299-329), float64, and the cache of the
+    backward.  p: A, B (standard) or U, V, M (-xs); m (dora-rows [out] / dora-cols [in]);
+    m_r [out] and m_c [in] (bora).  rms_norm(v, 1e-12) / sqrt(n) along a row of n values is
+    v / sqrt(sum v^2 + n * 1e-12)."""
+    fam, xs = split_adapter_type(adapter_type)
+    W = np.asarray(W, np.float64)
+    out, inn = W.shape
+    V = W + scale * mat_delta(p, xs)
+    c = {"fam": fam, "xs": xs, "V": V, "s": scale, "p": p}
+    if fam == "lora":
+        return V, c
+    if fam == "dora-rows":
+        m = np.asarray(p["m"], np.float64)
+        rn = np.sqrt((V * V).sum(1) + inn * MAT_EPS)
+        c.update(rn=rn, m=m)
+        return V * (m / rn)[:, None], c
+    if fam == "dora-cols":
+        m = np.asarray(p["m"], np.float64)
+        cn = np.sqrt((V * V).sum(0) + out * MAT_EPS)
+        c.update(cn=cn, m=m)
+        return V * (m / cn)[None, :], c
+    mr, mc = np.asarray(p["m_r"], np.float64), np.asarray(p["m_c"], np.float64)
+    rn = np.sqrt((V * V).sum(1) + inn * MAT_EPS)
+    R = V * (mr / rn)[:, None]
+    cn = np.sqrt((R * R).sum(0) + out * MAT_EPS)
+    c.update(rn=rn, cn=cn, R=R, m_r=mr, m_c=mc)
+    return R * (mc / cn)[None, :], c
+
+
+def mat_weight_grads(G, c):
+    """Gradients of the adapter parameters from G = dL/dW_eff [out][in]: dict with dA, dB
+    (standard) or dM (-xs), and dm (dora-rows, dora-cols) or dm_r, dm_c (bora).  The derivative
+    of v / n(v), n = sqrt(sum v^2 + k eps), along a row or column is (g - v <g, v> / n^2) / n."""
+    G = np.asarray(G, np.float64)
+    fam, V, p = c["fam"], c["V"], c["p"]
+    out = {}
+    if fam == "lora":
+        dV = G
+    elif fam == "dora-rows":
+        t = (G * V).sum(1)
+        out["dm"] = t / c["rn"]
+        dV = (c["m"] / c["rn"])[:, None] * (G - V * (t / c["rn"] ** 2)[:, None])
+    elif fam == "dora-cols":
+        t = (G * V).sum(0)
+        out["dm"] = t / c["cn"]
+        dV = (c["m"] / c["cn"])[None, :] * (G - V * (t / c["cn"] ** 2)[None, :])
+    else:
+        R, rn, cn = c["R"], c["rn"], c["cn"]
+        tc = (G * R).sum(0)
+        out["dm_c"] = tc / cn
+        dR = (c["m_c"] / cn)[None, :] * (G - R * (tc / cn ** 2)[None, :])
+        tr = (dR * V).sum(1)
+        out["dm_r"] = tr / rn
+        dV = (c["m_r"] / rn)[:, None] * (dR - V * (tr / rn ** 2)[:, None])
+    dD = c["s"] * dV
+    f = lambda k: np.asarray(p[k], np.float64)
+    if c["xs"]:
+        out["dM"] = f("U").T @ dD @ f("V")
+    else:
+        out["dB"] = dD @ f("A").T
+        out["dA"] = f("B").T @ dD
+    return out
+
+
+def mat_lin_fwd(x, W, p, adapter_type, scale, bias=None):
+    """y = x W_eff^T + bias through the materialized effective weight (src/train_dit.h:160-164:
+    the weight override that dit_lin then multiplies)."""
+    Weff, c = mat_effective_weight(W, p, adapter_type, scale)
+    x = np.asarray(x, np.float64)
+    y = x @ Weff.T
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)
+    c.update(x=x, Weff=Weff)
+    return y, c
+
+
+def mat_lin_bwd(dy, c):
+    """dx and the adapter gradients of mat_lin_fwd for upstream dy [S][out]."""
+    dy = np.asarray(dy, np.float64)
+    out = mat_weight_grads(dy.T @ c["x"], c)
+    out["dx"] = dy @ c["Weff"]
+    return out
 
 
 def functional_chain(W, terms, bns=None):

@@ -20,7 +20,7 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", os.path.join(os.path.dirname(HERE), "include")]
-SOURCES = ["quant.cu", "gemm_tc.cu", "gemm_r16.cu", "lora.cu", "adamw.cu", "attention.cu", "attention_tc.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu", "dp.cu", "gguf_io.cu", "checkpoint.cu", "lora_chain.cu"]
+SOURCES = ["quant.cu", "gemm_tc.cu", "gemm_r16.cu", "lora.cu", "adamw.cu", "attention.cu", "attention_tc.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu", "dp.cu", "gguf_io.cu", "checkpoint.cu", "lora_chain.cu", "materialize.cu"]
 
 
 def _compile(src, verbose):

@@ -1,0 +1,566 @@
+// materialize.cu -- linears whose adapter is applied through a materialized effective weight:
+// the families the trainer cannot apply functionally (dora-cols, bora, and the -xs forms of every
+// family, src/train_dit.h:90-164), and lora / dora-rows too when asked.
+//
+// Forward (src/train_lora.h:275-329), per call:
+//   V     = W + s * (B A)             or, for -xs, W + s * (U M) V^T      f32 [out][in]
+//   rows  rs[o] = m_r[o] / sqrt(sum_i V^2 + in * 1e-12)    (dora-rows: m, bora: m_r; else 1)
+//   cols  cs[i] = m_c[i] / sqrt(sum_o (rs V)^2 + out * 1e-12)  (dora-cols: m, bora: m_c; else 1)
+//   W_eff = rs[o] * V * cs[i], kept as the bf16 operand of the GEMMs
+//   y     = x W_eff^T + bias                                 (tcgen05 GEMM)
+// Backward:
+//   dx    = dy W_eff                                         (tcgen05 GEMM, W_eff read MN-major)
+//   G     = dy^T x                                           (tcgen05 GEMM, K = tokens)
+//   then through the column and row normalisations (the derivative of v / n(v) along a row or
+//   column is (g - v <g, v> / n^2) / n), dD = s dV, and the low-rank factors:
+//   dB = dD A^T, dA = B^T dD, or dM = U^T dD V for -xs (U, V frozen), dm / dm_r / dm_c.
+// The W-sized passes are HBM-bound f32 streams (V and G are each written once and read at most
+// twice); the three GEMMs carry the FLOPs.
+#include "../../include/sa3k.h"
+#include "linear.h"
+#include "lora_kernels.h"
+#include "sa3k_common.cuh"
+#include "sa3k_internal.h"
+#include "weight_value.cuh"
+
+#include <cstring>
+#include <string>
+
+namespace sa3k {
+namespace {
+
+constexpr float kMatEps = 1e-12f;
+constexpr int kMatRows = 8;        // rows per block of the row kernels (one warp per row)
+constexpr int kMatMaxRank = 16;
+constexpr int kSlotMat = 57;
+
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+__device__ __forceinline__ float warp_sumf(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// -xs: P = U M [out][r] (the row factor of the update) and Q = V^T [r][in].
+__global__ void mat_xs_prep_kernel(const float* __restrict__ U, const float* __restrict__ M,
+                                   const float* __restrict__ Vb, int64_t out, int64_t in, int r,
+                                   float* __restrict__ P, float* __restrict__ Q) {
+  const int64_t n1 = out * r, n = n1 + (int64_t)r * in;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+    if (k < n1) {
+      const int64_t o = k / r;
+      const int b = (int)(k % r);
+      float acc = 0.f;
+      for (int a = 0; a < r; ++a) acc = fmaf(U[o * r + a], M[a * r + b], acc);
+      P[k] = acc;
+    } else {
+      const int64_t q = k - n1;
+      Q[q] = Vb[(q % in) * r + q / in];
+    }
+  }
+}
+
+// V = W + s P Q, one warp per row; rn2[o] = sum_i V^2 + in eps (f64 sum) and rs[o] = mr[o] /
+// sqrt(rn2[o]) (1 without a row magnitude).  Q rows are read through L1 by the block's 8 rows.
+__global__ void __launch_bounds__(256) mat_build_kernel(const Weight w, const float* __restrict__ P,
+                                                        const float* __restrict__ Q, int r, float s,
+                                                        const float* __restrict__ mr, float* __restrict__ V,
+                                                        double* __restrict__ rn2, float* __restrict__ rs) {
+  __shared__ float ps[kMatRows][kMatMaxRank];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t o = (int64_t)blockIdx.x * kMatRows + warp;
+  if (o >= w.out) return;
+  if (lane < r) ps[warp][lane] = s * P[o * r + lane];
+  __syncwarp();
+  const int64_t in = w.in;
+  double acc = 0.0;
+  for (int64_t i = 4 * lane; i < in; i += 128) {
+    float v[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) v[c] = wval(w, o, i + c);
+    for (int j = 0; j < r; ++j) {
+      const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
+      const float pj = ps[warp][j];
+      v[0] = fmaf(pj, q.x, v[0]);
+      v[1] = fmaf(pj, q.y, v[1]);
+      v[2] = fmaf(pj, q.z, v[2]);
+      v[3] = fmaf(pj, q.w, v[3]);
+    }
+    *reinterpret_cast<float4*>(V + o * in + i) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc += (double)v[c] * (double)v[c];
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const double n2 = acc + (double)in * (double)kMatEps;
+    rn2[o] = n2;
+    rs[o] = mr ? mr[o] / (float)sqrt(n2) : 1.0f;
+  }
+}
+
+// Column sums over a slice of rows, added into acc[i] (f64 atomics):
+//   mode 0: sum_o (rs V)^2          (the column norms of the row-scaled V)
+//   mode 1: sum_o G (rs V)          (<g, r> along a column in the backward)
+__global__ void mat_colsum_kernel(const float* __restrict__ V, const float* __restrict__ G,
+                                  const float* __restrict__ rs, int64_t out, int64_t in, int64_t rows_per,
+                                  double* __restrict__ acc) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= in) return;
+  const int64_t o0 = (int64_t)blockIdx.y * rows_per, o1 = min(out, o0 + rows_per);
+  double a = 0.0;
+  for (int64_t o = o0; o < o1; ++o) {
+    const float rv = rs[o] * V[o * in + i];
+    a += G ? (double)G[o * in + i] * (double)rv : (double)rv * (double)rv;
+  }
+  if (o1 > o0) atomicAdd(acc + i, a);
+}
+
+// Column factors: cs[i] = mc[i] / cn[i] (1 without a column magnitude), cn^2 = csq + out eps.
+// With tc (the backward): cfac = cs, tcn[i] = tc / cn^2 and dmc[i] = tc / cn.
+__global__ void mat_colfac_kernel(const double* __restrict__ csq, const double* __restrict__ tc,
+                                  const float* __restrict__ mc, int64_t out, int64_t in, float* __restrict__ cs,
+                                  float* __restrict__ tcn, float* __restrict__ dmc) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= in) return;
+  if (!mc) {
+    cs[i] = 1.0f;
+    return;
+  }
+  const double n2 = csq[i] + (double)out * (double)kMatEps, n = sqrt(n2);
+  cs[i] = (float)((double)mc[i] / n);
+  if (tc) {
+    tcn[i] = (float)(tc[i] / n2);
+    if (dmc) dmc[i] = (float)(tc[i] / n);
+  }
+}
+
+// W_eff = rs[o] V cs[i] as bf16 (the GEMM operand) and, when asked, f32.
+__global__ void mat_weff_kernel(const float* __restrict__ V, const float* __restrict__ rs,
+                                const float* __restrict__ cs, int64_t out, int64_t in,
+                                __nv_bfloat16* __restrict__ wb, float* __restrict__ wf) {
+  const int64_t n4 = out * in / 4;
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n4; k += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = 4 * k, o = e / in, i = e % in;
+    const float4 v = reinterpret_cast<const float4*>(V)[k];
+    const float4 c = *reinterpret_cast<const float4*>(cs + i);
+    const float r = rs[o];
+    const float4 y = make_float4(r * v.x * c.x, r * v.y * c.y, r * v.z * c.z, r * v.w * c.w);
+    if (wf) reinterpret_cast<float4*>(wf)[k] = y;
+    uint2 p;
+    p.x = pack_bf16x2(y.x, y.y);
+    p.y = pack_bf16x2(y.z, y.w);
+    reinterpret_cast<uint2*>(wb)[k] = p;
+  }
+}
+
+// dst[o][s] = bf16(src[s][o]) (src [S][out] f32 -> dst [out][ld] bf16), 32 x 32 tiles.
+__global__ void transpose_bf16_kernel(const float* __restrict__ src, int64_t S, int64_t out,
+                                      __nv_bfloat16* __restrict__ dst, int64_t ld) {
+  __shared__ float t[32][33];
+  const int64_t s0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t s = s0 + k, o = o0 + threadIdx.x;
+    t[k][threadIdx.x] = (s < S && o < out) ? src[s * out + o] : 0.f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t o = o0 + k, s = s0 + threadIdx.x;
+    if (o < out && s < S) dst[o * ld + s] = __float2bfloat16_rn(t[threadIdx.x][k]);
+  }
+}
+
+// The row pass of the backward, one warp per row o, G [out][in] replaced by dD = s dV:
+//   dR = cols ? cs[i] (G - rs V tcn[i]) : G
+//   rows: t = sum_i dR V, dmr[o] = t / rn, dV = rs (dR - V t / rn^2), else dV = dR
+//   PG[o][j] = sum_i dD Q[j][i] (dB for the standard families, (dD V)[o][j] for -xs).
+__global__ void __launch_bounds__(256) mat_rowbwd_kernel(float* __restrict__ G, const float* __restrict__ V,
+                                                         const float* __restrict__ rs, const double* __restrict__ rn2,
+                                                         const float* __restrict__ cs, const float* __restrict__ tcn,
+                                                         const float* __restrict__ Q, int64_t out, int64_t in, int r,
+                                                         float s, int rows, int cols, float* __restrict__ dmr,
+                                                         float* __restrict__ PG) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t o = (int64_t)blockIdx.x * kMatRows + warp;
+  if (o >= out) return;
+  float* g = G + o * in;
+  const float* v = V + o * in;
+  const float ro = rs[o];
+  auto dR = [&](int64_t i, float gv, float vv) -> float {
+    return cols ? cs[i] * (gv - ro * vv * tcn[i]) : gv;
+  };
+  float t_over = 0.f;
+  if (rows) {
+    double t = 0.0;
+    for (int64_t i = 4 * lane; i < in; i += 128) {
+      const float4 gv = *reinterpret_cast<const float4*>(g + i), vv = *reinterpret_cast<const float4*>(v + i);
+      t += (double)dR(i, gv.x, vv.x) * vv.x + (double)dR(i + 1, gv.y, vv.y) * vv.y +
+           (double)dR(i + 2, gv.z, vv.z) * vv.z + (double)dR(i + 3, gv.w, vv.w) * vv.w;
+    }
+    t = warp_sum(t);
+    if (lane == 0) dmr[o] = (float)(t / sqrt(rn2[o]));
+    t_over = (float)(t / rn2[o]);
+  }
+  float acc[kMatMaxRank];
+#pragma unroll
+  for (int j = 0; j < kMatMaxRank; ++j) acc[j] = 0.f;
+  for (int64_t i = 4 * lane; i < in; i += 128) {
+    const float4 gv = *reinterpret_cast<const float4*>(g + i), vv = *reinterpret_cast<const float4*>(v + i);
+    float d[4] = {dR(i, gv.x, vv.x), dR(i + 1, gv.y, vv.y), dR(i + 2, gv.z, vv.z), dR(i + 3, gv.w, vv.w)};
+    const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) d[c] = s * (rows ? ro * (d[c] - vx[c] * t_over) : d[c]);
+    *reinterpret_cast<float4*>(g + i) = make_float4(d[0], d[1], d[2], d[3]);
+#pragma unroll
+    for (int j = 0; j < kMatMaxRank; ++j) {
+      if (j >= r) break;
+      const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
+      acc[j] = fmaf(d[0], q.x, fmaf(d[1], q.y, fmaf(d[2], q.z, fmaf(d[3], q.w, acc[j]))));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kMatMaxRank; ++j) {
+    if (j >= r) break;
+    const float a = warp_sumf(acc[j]);
+    if (lane == 0) PG[o * r + j] = a;
+  }
+}
+
+// dA[j][i] += sum_{o in slice} B[o][j] dD[o][i] (f32 atomics; dA zeroed first).
+__global__ void __launch_bounds__(256) mat_da_kernel(const float* __restrict__ dD, const float* __restrict__ B,
+                                                     int64_t out, int64_t in, int r, int64_t rows_per,
+                                                     float* __restrict__ dA) {
+  __shared__ float bs[64][kMatMaxRank];
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t o0 = (int64_t)blockIdx.y * rows_per, o1 = min(out, o0 + rows_per);
+  float acc[kMatMaxRank];
+#pragma unroll
+  for (int j = 0; j < kMatMaxRank; ++j) acc[j] = 0.f;
+  for (int64_t ob = o0; ob < o1; ob += 64) {
+    const int nb = (int)min((int64_t)64, o1 - ob);
+    __syncthreads();
+    for (int k = threadIdx.x; k < nb * r; k += blockDim.x) bs[k / r][k % r] = B[(ob + k / r) * r + k % r];
+    __syncthreads();
+    if (i < in) {
+      for (int q = 0; q < nb; ++q) {
+        const float d = dD[(ob + q) * in + i];
+#pragma unroll
+        for (int j = 0; j < kMatMaxRank; ++j) {
+          if (j >= r) break;
+          acc[j] = fmaf(bs[q][j], d, acc[j]);
+        }
+      }
+    }
+  }
+  if (i < in && o1 > o0) {
+#pragma unroll
+    for (int j = 0; j < kMatMaxRank; ++j) {
+      if (j >= r) break;
+      atomicAdd(dA + (int64_t)j * in + i, acc[j]);
+    }
+  }
+}
+
+// dM[a][b] = sum_o U[o][a] PG[o][b] (PG = dD V), one block per (a, b).
+__global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __restrict__ PG, int64_t out, int r,
+                                 float* __restrict__ dM) {
+  const int a = blockIdx.x / r, b = blockIdx.x % r;
+  float acc = 0.f;
+  for (int64_t o = threadIdx.x; o < out; o += blockDim.x) acc = fmaf(U[o * r + a], PG[o * r + b], acc);
+  __shared__ float red[32];
+  acc = warp_sumf(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sumf(v);
+    if (threadIdx.x == 0) dM[blockIdx.x] = v;
+  }
+}
+
+struct MatPlan {
+  bool xs = false, rows = false, cols = false;
+  const float* mr = nullptr;   // row magnitude (dora-rows m, bora m_r)
+  const float* mc = nullptr;   // column magnitude (dora-cols m, bora m_c)
+};
+
+bool parse_type(const sa3k_mat_adapter* ad, MatPlan& p, std::string& err) {
+  if (!ad->adapter_type) {
+    err = "adapter_type is NULL";
+    return false;
+  }
+  std::string t = ad->adapter_type;
+  p.xs = t.size() >= 3 && t.compare(t.size() - 3, 3, "-xs") == 0;
+  if (p.xs) t = t.substr(0, t.size() - 3);
+  if (t == "lora") {
+  } else if (t == "dora-rows") {
+    p.rows = true;
+    p.mr = ad->m;
+  } else if (t == "dora-cols") {
+    p.cols = true;
+    p.mc = ad->m;
+  } else if (t == "bora") {
+    p.rows = p.cols = true;
+    p.mr = ad->m_r;
+    p.mc = ad->m_c;
+  } else {
+    err = "unknown adapter_type " + std::string(ad->adapter_type);
+    return false;
+  }
+  if ((p.rows && !p.mr) || (p.cols && !p.mc)) {
+    err = "adapter magnitude missing for " + std::string(ad->adapter_type);
+    return false;
+  }
+  if (ad->rank < 1 || ad->rank > kMatMaxRank) {
+    err = "materialized adapters take rank 1..16";
+    return false;
+  }
+  if (p.xs ? (!ad->U || !ad->V || !ad->M) : (!ad->A || !ad->B)) {
+    err = p.xs ? "-xs adapters need U, V and M" : "adapters need A and B";
+    return false;
+  }
+  if (!p.xs && (reinterpret_cast<uintptr_t>(ad->A) & 15)) {
+    err = "A must be 16-byte aligned";
+    return false;
+  }
+  return true;
+}
+
+// Device buffers of one call, carved from one scratch slot.
+struct MatBufs {
+  float *V, *G, *P, *Q, *PG, *rs, *cs, *tcn;
+  double *rn2, *csq, *tc;
+  __nv_bfloat16 *wb, *xb, *dyb, *dyt;
+  int64_t ldt;
+};
+
+bool mat_alloc(Ctx* c, int64_t S, int64_t in, int64_t out, int r, bool bwd, MatBufs& b, std::string& err) {
+  const int64_t wn = out * in;
+  b.ldt = (S + 7) / 8 * 8;
+  size_t off = 0;
+  auto take = [&](size_t bytes) { const size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
+  const size_t oV = take(4 * wn), oG = bwd ? take(4 * wn) : 0, oP = take(4 * (size_t)out * r),
+               oQ = take(4 * (size_t)r * in), oPG = take(4 * (size_t)out * r), ors = take(4 * out),
+               ocs = take(4 * in), otcn = take(4 * in), orn2 = take(8 * out), ocsq = take(8 * in),
+               otc = take(8 * in), owb = take(2 * wn), oxb = take(2 * (size_t)S * in),
+               odyb = bwd ? take(2 * (size_t)S * out) : 0, odyt = bwd ? take(2 * (size_t)out * b.ldt) : 0;
+  uint8_t* base = static_cast<uint8_t*>(scratch_get(c, kSlotMat, off, err));
+  if (!base) return false;
+  b.V = reinterpret_cast<float*>(base + oV);
+  b.G = bwd ? reinterpret_cast<float*>(base + oG) : nullptr;
+  b.P = reinterpret_cast<float*>(base + oP);
+  b.Q = reinterpret_cast<float*>(base + oQ);
+  b.PG = reinterpret_cast<float*>(base + oPG);
+  b.rs = reinterpret_cast<float*>(base + ors);
+  b.cs = reinterpret_cast<float*>(base + ocs);
+  b.tcn = reinterpret_cast<float*>(base + otcn);
+  b.rn2 = reinterpret_cast<double*>(base + orn2);
+  b.csq = reinterpret_cast<double*>(base + ocsq);
+  b.tc = reinterpret_cast<double*>(base + otc);
+  b.wb = reinterpret_cast<__nv_bfloat16*>(base + owb);
+  b.xb = reinterpret_cast<__nv_bfloat16*>(base + oxb);
+  b.dyb = bwd ? reinterpret_cast<__nv_bfloat16*>(base + odyb) : nullptr;
+  b.dyt = bwd ? reinterpret_cast<__nv_bfloat16*>(base + odyt) : nullptr;
+  return true;
+}
+
+// Slices of rows for the column kernels: about two blocks of 256 columns per SM.
+int64_t col_rows_per(Ctx* c, int64_t out, int64_t in) {
+  const int64_t cb = (in + 255) / 256;
+  int64_t splits = (int64_t)(2 * c->sm_count) / cb;
+  splits = splits < 1 ? 1 : (splits > out ? out : splits);
+  return (out + splits - 1) / splits;
+}
+
+// V, the row and column factors and W_eff (bf16 in b.wb; f32 into weff_f32 when not null).
+int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, MatBufs& b,
+               float* weff_f32, std::string& err) {
+  const int64_t in = w->in, out = w->out;
+  const int r = ad->rank;
+  const cudaStream_t st = c->stream;
+  const float* P = ad->B;
+  const float* Q = ad->A;
+  if (p.xs) {
+    ProfScope prof_(c, "mat.xs_prep");
+    mat_xs_prep_kernel<<<(unsigned)(2 * c->sm_count), 256, 0, st>>>(ad->U, ad->M, ad->V, out, in, r, b.P, b.Q);
+    if (check_launch("mat xs prep", err)) return 1;
+    P = b.P;
+    Q = b.Q;
+  }
+  {
+    ProfScope prof_(c, "mat.build");
+    mat_build_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(*w, P, Q, r, ad->scale, p.mr, b.V,
+                                                                                  b.rn2, b.rs);
+    if (check_launch("mat build", err)) return 1;
+  }
+  if (p.cols) {
+    ProfScope prof_(c, "mat.cols");
+    if (cudaMemsetAsync(b.csq, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
+    const int64_t rp = col_rows_per(c, out, in);
+    mat_colsum_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
+        b.V, nullptr, b.rs, out, in, rp, b.csq);
+    if (check_launch("mat colsum", err)) return 1;
+  }
+  {
+    ProfScope prof_(c, "mat.weff");
+    mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, nullptr, p.mc, out, in, b.cs, nullptr,
+                                                                   nullptr);
+    if (check_launch("mat colfac", err)) return 1;
+    mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(b.V, b.rs, b.cs, out, in, b.wb, weff_f32);
+    if (check_launch("mat weff", err)) return 1;
+  }
+  return 0;
+}
+
+int mat_check(const sa3k_weight* w, const sa3k_mat_adapter* ad, int64_t S, MatPlan& p, std::string& err) {
+  if (!parse_type(ad, p, err)) return 1;
+  if (w->w.in % 64 != 0) {
+    err = "in must be a multiple of 64";
+    return 1;
+  }
+  if (S < 0) {
+    err = "S must be positive";
+    return 1;
+  }
+  return 0;
+}
+
+int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, const float* bias, const float* x,
+            const float* dy, int64_t S, float* y, float* dx, const sa3k_mat_grads* g, std::string& err) {
+  const int64_t in = w->in, out = w->out;
+  const int r = ad->rank;
+  const cudaStream_t st = c->stream;
+  const bool bwd = dy != nullptr;
+  MatBufs b;
+  if (!mat_alloc(c, S, in, out, r, bwd, b, err)) return 1;
+  if (mat_weight(c, w, ad, p, b, nullptr, err)) return 1;
+  if (k_cvt_bf16(c, x, S * in, b.xb, err)) return 1;
+  if (y) {
+    GemmDesc d;   // y = x W_eff^T + bias
+    d.M = (int)S; d.N = (int)out; d.K = (int)in;
+    d.a = b.xb; d.lda = in;
+    d.bsrc = kB_BF16_KMAJOR; d.b = b.wb; d.ldb = in;
+    d.col_bias = bias;
+    d.out = y; d.ldo = out;
+    d.name = "mat.fwd";
+    if (gemm(c, d, err)) return 1;
+  }
+  if (!bwd) return 0;
+  if (k_cvt_bf16(c, dy, S * out, b.dyb, err)) return 1;
+  if (dx) {
+    GemmDesc d;   // dx = dy W_eff
+    d.M = (int)S; d.N = (int)in; d.K = (int)out;
+    d.a = b.dyb; d.lda = out;
+    d.bsrc = kB_BF16_MNMAJOR; d.b = b.wb; d.ldb = in;
+    d.out = dx; d.ldo = in;
+    d.name = "mat.dx";
+    if (gemm(c, d, err)) return 1;
+  }
+  {
+    ProfScope prof_(c, "mat.transpose");
+    transpose_bf16_kernel<<<dim3((unsigned)((S + 31) / 32), (unsigned)((out + 31) / 32)), dim3(32, 8), 0, st>>>(
+        dy, S, out, b.dyt, b.ldt);
+    if (check_launch("mat transpose", err)) return 1;
+  }
+  {
+    GemmDesc d;   // G = dy^T x  [out][in], K = tokens
+    d.M = (int)out; d.N = (int)in; d.K = (int)S;
+    d.a = b.dyt; d.lda = b.ldt;
+    d.bsrc = kB_BF16_MNMAJOR; d.b = b.xb; d.ldb = in;
+    d.out = b.G; d.ldo = in;
+    d.name = "mat.dW";
+    if (gemm(c, d, err)) return 1;
+  }
+  const float* Q = p.xs ? b.Q : ad->A;
+  if (p.cols) {
+    ProfScope prof_(c, "mat.cols_bwd");
+    if (cudaMemsetAsync(b.tc, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
+    const int64_t rp = col_rows_per(c, out, in);
+    mat_colsum_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
+        b.V, b.G, b.rs, out, in, rp, b.tc);
+    if (check_launch("mat colsum bwd", err)) return 1;
+    mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, b.tc, p.mc, out, in, b.cs, b.tcn,
+                                                                   p.rows ? g->dm_c : g->dm);
+    if (check_launch("mat colfac bwd", err)) return 1;
+  }
+  {
+    ProfScope prof_(c, "mat.rows_bwd");
+    mat_rowbwd_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(
+        b.G, b.V, b.rs, b.rn2, b.cs, b.tcn, Q, out, in, r, ad->scale, p.rows ? 1 : 0, p.cols ? 1 : 0,
+        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB);
+    if (check_launch("mat rows bwd", err)) return 1;
+  }
+  if (p.xs) {
+    ProfScope prof_(c, "mat.dM");
+    mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(ad->U, b.PG, out, r, g->dM);
+    return check_launch("mat dM", err);
+  }
+  ProfScope prof_(c, "mat.dA");
+  if (cudaMemsetAsync(g->dA, 0, sizeof(float) * (size_t)r * in, st) != cudaSuccess) return check_launch("memset", err);
+  const int64_t rp = col_rows_per(c, out, in);
+  mat_da_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
+      b.G, ad->B, out, in, r, rp, g->dA);
+  return check_launch("mat dA", err);
+}
+
+int mfail(char* err, int len, const std::string& msg) {
+  if (err && len > 0) {
+    std::strncpy(err, msg.c_str(), (size_t)len - 1);
+    err[len - 1] = 0;
+  }
+  return 1;
+}
+
+}  // namespace
+}  // namespace sa3k
+
+using namespace sa3k;
+
+extern "C" {
+
+int sa3k_mat_effective_weight(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, float* weff,
+                              char* err, int err_len) {
+  if (!ctx || !w || !ad || !weff) return mfail(err, err_len, "NULL argument");
+  MatPlan p;
+  std::string e;
+  if (mat_check(w, ad, 1, p, e)) return mfail(err, err_len, e);
+  Ctx* c = &ctx->c;
+  cudaSetDevice(c->device);
+  MatBufs b;
+  if (!mat_alloc(c, 1, w->w.in, w->w.out, ad->rank, false, b, e) || mat_weight(c, &w->w, ad, p, b, weff, e))
+    return mfail(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_mat_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, const float* bias,
+                        const float* x, int64_t S, float* y, char* err, int err_len) {
+  if (!ctx || !w || !ad || !x || !y) return mfail(err, err_len, "NULL argument");
+  if (S <= 0) return mfail(err, err_len, "S must be positive");
+  MatPlan p;
+  std::string e;
+  if (mat_check(w, ad, S, p, e)) return mfail(err, err_len, e);
+  cudaSetDevice(ctx->c.device);
+  if (mat_run(&ctx->c, &w->w, ad, p, bias, x, nullptr, S, y, nullptr, nullptr, e)) return mfail(err, err_len, e);
+  return 0;
+}
+
+int sa3k_linear_mat_fwd_bwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_mat_adapter* ad, const float* bias,
+                            const float* x, const float* dy, int64_t S, float* y, float* dx, const sa3k_mat_grads* g,
+                            char* err, int err_len) {
+  if (!ctx || !w || !ad || !x || !dy || !g) return mfail(err, err_len, "NULL argument");
+  if (S <= 0) return mfail(err, err_len, "S must be positive");
+  MatPlan p;
+  std::string e;
+  if (mat_check(w, ad, S, p, e)) return mfail(err, err_len, e);
+  if (p.xs ? !g->dM : (!g->dA || !g->dB)) return mfail(err, err_len, p.xs ? "-xs adapters need dM" : "need dA and dB");
+  if (p.rows && p.cols ? (!g->dm_r || !g->dm_c) : ((p.rows || p.cols) && !g->dm))
+    return mfail(err, err_len, "magnitude gradients missing");
+  cudaSetDevice(ctx->c.device);
+  if (mat_run(&ctx->c, &w->w, ad, p, bias, x, dy, S, y, dx, g, e)) return mfail(err, err_len, e);
+  return 0;
+}
+
+}  // extern "C"

@@ -11,6 +11,7 @@
 // value(o, i) = code * d (Q8_0) or (d*sc) * code - dmin*m (Q4_K) in f32 is exactly what
 // ggml-quants.c computes; dequant_kernel below is the bit-exactness probe for that claim.
 #include "sa3k_internal.h"
+#include "weight_value.cuh"
 
 namespace sa3k {
 
@@ -80,24 +81,6 @@ __global__ void repack_f16_kernel(const __half* __restrict__ src, int64_t n, __n
 __global__ void repack_f32_kernel(const float* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     dst[i] = __float2bfloat16_rn(src[i]);
-}
-
-// Dequantized value of (o, i) from the device layout, f32, bit-identical to ggml's to_float.
-__device__ __forceinline__ float wval(const Weight& w, int64_t o, int64_t i) {
-  switch (w.type) {
-    case kTypeQ8_0:
-      return (float)w.codes[o * w.in + i] * w.scales[(i >> 5) * w.out + o];
-    case kTypeQ4_K: {
-      const uint8_t b = reinterpret_cast<const uint8_t*>(w.codes)[o * (w.in / 2) + (i >> 1)];
-      const int q = (i & 1) ? (b >> 4) : (b & 15);
-      const float2 s = reinterpret_cast<const float2*>(w.scales)[(i >> 5) * w.out + o];
-      return s.x * (float)q - s.y;
-    }
-    case kTypeF16:
-      return __half2float(reinterpret_cast<const __half*>(w.raw)[o * w.in + i]);
-    default:
-      return reinterpret_cast<const float*>(w.raw)[o * w.in + i];
-  }
 }
 
 __global__ void dequant_kernel(const Weight w, float* __restrict__ dst) {

@@ -3,11 +3,12 @@ attention of the DiT step's shape, run a few times through the C ABI, so that a 
 (ncu -k regex:gemm_tc -c 1) sees a handful of launches of one kernel on a few hundred MB.
 
     python sa3.cpp_b200/kernel_cases.py gemm --m 4352 --n 1536 --k 1536 [--dx] [--qtype q8_0]
-        [--pair 0|1|2] [--tile-n 0|128|192|256] [--adapter] [--reps 3] [--time]
+        [--pair 0|1|2] [--tile-n 0|128|192|256] [--adapter] [--smem-dequant] [--reps 3] [--time]
 
 --dx runs the input-gradient GEMM dx[m][k] = dy[m][n] . W[n][k] of a linear with in = k,
 out = n (the weight is used transposed); the default is the forward y = x W^T + 0.
 --adapter adds a rank-16 LoRA adapter (the forward then also runs u = x A^T).
+--smem-dequant reads a quantized base as its codes, dequantized in shared memory.
 
     python sa3.cpp_b200/kernel_cases.py attention [--b 4 --h 24 --s 1088 --window -1] [--fwd-only]
 --time prints the CUDA-event time per launch (not to be used under a profiler)."""
@@ -27,6 +28,7 @@ def gemm_case(a):
     ctx = sa3k.Context(0)
     ctx.set_option(sa3k.OPT_GEMM_PAIR, a.pair)
     ctx.set_option(sa3k.OPT_GEMM_TILE_N, a.tile_n)
+    ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 1 if a.smem_dequant else 0)
     g = torch.Generator().manual_seed(0)
     W = torch.randn(a.n, a.k, generator=g) * 0.02                 # [out = n][in = k]
     if a.qtype == "f32":
@@ -120,6 +122,7 @@ def main():
     gp.add_argument("--pair", type=int, default=1)
     gp.add_argument("--tile-n", type=int, default=0)
     gp.add_argument("--adapter", action="store_true")
+    gp.add_argument("--smem-dequant", action="store_true")
     gp.add_argument("--warmup", type=int, default=2)
     gp.add_argument("--reps", type=int, default=3)
     gp.add_argument("--time", action="store_true")

@@ -29,7 +29,8 @@ ABI_SYMBOLS = (
     "sa3k_dit_dp_apply_adamw", "sa3k_dit_save_adapter", "sa3k_dit_load_adapter", "sa3k_dit_save_checkpoint",
     "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
     "sa3k_gguf_get_u64_array", "sa3k_gguf_get_f32", "sa3k_lora_chain_build", "sa3k_lora_chain_free",
-    "sa3k_lora_chain_info", "sa3k_linear_fwd_chain",
+    "sa3k_lora_chain_info", "sa3k_linear_fwd_chain", "sa3k_mat_effective_weight", "sa3k_linear_mat_fwd",
+    "sa3k_linear_mat_fwd_bwd",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
@@ -75,6 +76,24 @@ class ChainTerm(ctypes.Structure):
     """sa3k_chain_term: one adapter of an inference chain (device pointers)."""
     _fields_ = [("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("magnitude", ctypes.c_void_p), ("rank", ctypes.c_int),
                 ("scale", ctypes.c_float)]
+
+
+class MatAdapter(ctypes.Structure):
+    """sa3k_mat_adapter: a materialized adapter of any family ("lora", "dora-rows", "dora-cols",
+    "bora", each optionally "-xs"); every array a device pointer."""
+    _fields_ = [("adapter_type", ctypes.c_char_p), ("rank", ctypes.c_int), ("scale", ctypes.c_float),
+                ("A", ctypes.c_void_p), ("B", ctypes.c_void_p), ("U", ctypes.c_void_p), ("V", ctypes.c_void_p),
+                ("M", ctypes.c_void_p), ("m", ctypes.c_void_p), ("m_r", ctypes.c_void_p), ("m_c", ctypes.c_void_p)]
+
+
+class MatGrads(ctypes.Structure):
+    """sa3k_mat_grads: the gradient outputs of sa3k_linear_mat_fwd_bwd (NULL where unused)."""
+    _fields_ = [("dA", ctypes.c_void_p), ("dB", ctypes.c_void_p), ("dM", ctypes.c_void_p), ("dm", ctypes.c_void_p),
+                ("dm_r", ctypes.c_void_p), ("dm_c", ctypes.c_void_p)]
+
+
+def _vp(t):
+    return None if t is None else t.data_ptr()
 
 
 class TrainProgress(ctypes.Structure):
@@ -155,6 +174,10 @@ def lib():
         L.sa3k_lora_chain_free.restype = None
         L.sa3k_lora_chain_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
         L.sa3k_linear_fwd_chain.argtypes = [P, P, P, P, P, I64, P, E, I]
+        L.sa3k_mat_effective_weight.argtypes = [P, P, ctypes.POINTER(MatAdapter), P, E, I]
+        L.sa3k_linear_mat_fwd.argtypes = [P, P, ctypes.POINTER(MatAdapter), P, P, I64, P, E, I]
+        L.sa3k_linear_mat_fwd_bwd.argtypes = [P, P, ctypes.POINTER(MatAdapter), P, P, P, I64, P, P,
+                                              ctypes.POINTER(MatGrads), E, I]
         L.sa3k_dit_save_adapter.argtypes = [P, E, E, I]
         L.sa3k_dit_load_adapter.argtypes = [P, E, E, I]
         L.sa3k_dit_save_checkpoint.argtypes = [P, E, E, I64, ctypes.POINTER(TrainProgress), E, I]
@@ -324,6 +347,28 @@ class Context:
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_linear_fwd_chain(self._h, w._h, chain._h, _ptr(bias), _ptr(x), x.shape[0], _ptr(y), err,
                                            512), err)
+
+    @staticmethod
+    def mat_adapter(adapter_type, rank, scale, A=None, B=None, U=None, V=None, M=None, m=None, m_r=None, m_c=None):
+        """A MatAdapter over device tensors (kept alive by the caller)."""
+        return MatAdapter(adapter_type.encode(), rank, scale, _vp(A), _vp(B), _vp(U), _vp(V), _vp(M), _vp(m), _vp(m_r),
+                          _vp(m_c))
+
+    def mat_effective_weight(self, w, ad, weff):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_mat_effective_weight(self._h, w._h, ctypes.byref(ad), _ptr(weff), err, 512), err)
+
+    def linear_mat_fwd(self, w, ad, x, y, bias=None):
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_linear_mat_fwd(self._h, w._h, ctypes.byref(ad), _ptr(bias), _ptr(x), x.shape[0], _ptr(y),
+                                         err, 512), err)
+
+    def linear_mat_fwd_bwd(self, w, ad, x, dy, y=None, dx=None, bias=None, dA=None, dB=None, dM=None, dm=None,
+                           dm_r=None, dm_c=None):
+        err = ctypes.create_string_buffer(512)
+        g = MatGrads(_vp(dA), _vp(dB), _vp(dM), _vp(dm), _vp(dm_r), _vp(dm_c))
+        _check(lib().sa3k_linear_mat_fwd_bwd(self._h, w._h, ctypes.byref(ad), _ptr(bias), _ptr(x), _ptr(dy),
+                                             x.shape[0], _ptr(y), _ptr(dx), ctypes.byref(g), err, 512), err)
 
     def linear_bwd(self, w, x, y, dy, dx, ad=None, bias=None, dA=None, dB=None, dm=None, accumulate=False):
         err = ctypes.create_string_buffer(512)
