@@ -102,21 +102,45 @@ __global__ void __launch_bounds__(256) mat_build_kernel(const Weight w, const fl
   }
 }
 
-// Column sums over a slice of rows, added into acc[i] (f64 atomics):
-//   mode 0: sum_o (rs V)^2          (the column norms of the row-scaled V)
-//   mode 1: sum_o G (rs V)          (<g, r> along a column in the backward)
-__global__ void mat_colsum_kernel(const float* __restrict__ V, const float* __restrict__ G,
-                                  const float* __restrict__ rs, int64_t out, int64_t in, int64_t rows_per,
-                                  double* __restrict__ acc) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+// Column sums over a slice of rows, added into acc[i] (f64 atomics), four columns per thread and
+// four rows of loads in flight:
+//   G null: sum_o (rs V)^2          (the column norms of the row-scaled V)
+//   else:   sum_o G (rs V)          (<g, r> along a column in the backward)
+constexpr int kColThreads = 128;
+__global__ void __launch_bounds__(kColThreads) mat_colsum_kernel(const float* __restrict__ V, const float* __restrict__ G,
+                                                                 const float* __restrict__ rs, int64_t out, int64_t in,
+                                                                 int64_t rows_per, double* __restrict__ acc) {
+  const int64_t i = 4 * ((int64_t)blockIdx.x * blockDim.x + threadIdx.x);
   if (i >= in) return;
   const int64_t o0 = (int64_t)blockIdx.y * rows_per, o1 = min(out, o0 + rows_per);
-  double a = 0.0;
-  for (int64_t o = o0; o < o1; ++o) {
-    const float rv = rs[o] * V[o * in + i];
-    a += G ? (double)G[o * in + i] * (double)rv : (double)rv * (double)rv;
+  double a[4] = {0.0, 0.0, 0.0, 0.0};
+  auto add = [&](const float4& v, const float4& g, float r) {
+    const float rv[4] = {r * v.x, r * v.y, r * v.z, r * v.w};
+    const float gv[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) a[c] += G ? (double)gv[c] * (double)rv[c] : (double)rv[c] * (double)rv[c];
+  };
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  int64_t o = o0;
+  for (; o + 4 <= o1; o += 4) {
+    float4 v[4], g[4];
+    float r[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      v[u] = *reinterpret_cast<const float4*>(V + (o + u) * in + i);
+      g[u] = G ? *reinterpret_cast<const float4*>(G + (o + u) * in + i) : zero;
+      r[u] = rs[o + u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) add(v[u], g[u], r[u]);
   }
-  if (o1 > o0) atomicAdd(acc + i, a);
+  for (; o < o1; ++o)
+    add(*reinterpret_cast<const float4*>(V + o * in + i), G ? *reinterpret_cast<const float4*>(G + o * in + i) : zero,
+        rs[o]);
+  if (o1 > o0) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) atomicAdd(acc + i + c, a[c]);
+  }
 }
 
 // Column factors: cs[i] = mc[i] / cn[i] (1 without a column magnitude), cn^2 = csq + out eps.
@@ -173,59 +197,126 @@ __global__ void transpose_bf16_kernel(const float* __restrict__ src, int64_t S, 
   }
 }
 
-// The row pass of the backward, one warp per row o, G [out][in] replaced by dD = s dV:
+// The row pass of the backward, G [out][in] replaced by dD = s dV:
 //   dR = cols ? cs[i] (G - rs V tcn[i]) : G
 //   rows: t = sum_i dR V, dmr[o] = t / rn, dV = rs (dR - V t / rn^2), else dV = dR
 //   PG[o][j] = sum_i dD Q[j][i] (dB for the standard families, (dD V)[o][j] for -xs).
-__global__ void __launch_bounds__(256) mat_rowbwd_kernel(float* __restrict__ G, const float* __restrict__ V,
-                                                         const float* __restrict__ rs, const double* __restrict__ rn2,
-                                                         const float* __restrict__ cs, const float* __restrict__ tcn,
-                                                         const float* __restrict__ Q, int64_t out, int64_t in, int r,
-                                                         float s, int rows, int cols, float* __restrict__ dmr,
-                                                         float* __restrict__ PG) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t o = (int64_t)blockIdx.x * kMatRows + warp;
-  if (o >= out) return;
-  float* g = G + o * in;
-  const float* v = V + o * in;
-  const float ro = rs[o];
-  auto dR = [&](int64_t i, float gv, float vv) -> float {
-    return cols ? cs[i] * (gv - ro * vv * tcn[i]) : gv;
-  };
-  float t_over = 0.f;
-  if (rows) {
-    double t = 0.0;
-    for (int64_t i = 4 * lane; i < in; i += 128) {
-      const float4 gv = *reinterpret_cast<const float4*>(g + i), vv = *reinterpret_cast<const float4*>(v + i);
-      t += (double)dR(i, gv.x, vv.x) * vv.x + (double)dR(i + 1, gv.y, vv.y) * vv.y +
-           (double)dR(i + 2, gv.z, vv.z) * vv.z + (double)dR(i + 3, gv.w, vv.w) * vv.w;
-    }
-    t = warp_sum(t);
-    if (lane == 0) dmr[o] = (float)(t / sqrt(rn2[o]));
-    t_over = (float)(t / rn2[o]);
+// A block of 128 threads takes two rows, its threads spread over the columns (many warps per SM
+// even for 1536-row weights); each Q chunk read serves both rows, and the row sums are reduced
+// through shared memory.
+constexpr int kRbThreads = 128, kRbRows = 2, kRbWarps = kRbThreads / 32;
+__global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restrict__ G, const float* __restrict__ V,
+                                                                const float* __restrict__ rs,
+                                                                const double* __restrict__ rn2,
+                                                                const float* __restrict__ cs,
+                                                                const float* __restrict__ tcn,
+                                                                const float* __restrict__ Q, int64_t out, int64_t in,
+                                                                int r, float s, int rows, int cols,
+                                                                float* __restrict__ dmr, float* __restrict__ PG) {
+  __shared__ double red_t[kRbWarps][kRbRows];
+  __shared__ float red_a[kRbWarps][kRbRows * kMatMaxRank];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t o0 = (int64_t)blockIdx.x * kRbRows;
+  const int nr = (int)min((int64_t)kRbRows, out - o0);
+  float ro[kRbRows], t_over[kRbRows];
+#pragma unroll
+  for (int u = 0; u < kRbRows; ++u) {
+    ro[u] = u < nr ? rs[o0 + u] : 0.f;
+    t_over[u] = 0.f;
   }
-  float acc[kMatMaxRank];
+  // dR of 4 columns of row u (cf / tc: the column factors of those columns)
+  auto dr4 = [&](const float4& gv, const float4& vv, const float4& cf, const float4& tc, float r0, float (&d)[4]) {
+    if (cols) {
+      d[0] = cf.x * (gv.x - r0 * vv.x * tc.x);
+      d[1] = cf.y * (gv.y - r0 * vv.y * tc.y);
+      d[2] = cf.z * (gv.z - r0 * vv.z * tc.z);
+      d[3] = cf.w * (gv.w - r0 * vv.w * tc.w);
+    } else {
+      d[0] = gv.x; d[1] = gv.y; d[2] = gv.z; d[3] = gv.w;
+    }
+  };
+  const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
+  if (rows) {
+    double t[kRbRows] = {0.0, 0.0};
+    for (int64_t i = 4 * tid; i < in; i += 4 * kRbThreads) {
+      const float4 cf = cols ? *reinterpret_cast<const float4*>(cs + i) : one4;
+      const float4 tc = cols ? *reinterpret_cast<const float4*>(tcn + i) : one4;
 #pragma unroll
-  for (int j = 0; j < kMatMaxRank; ++j) acc[j] = 0.f;
-  for (int64_t i = 4 * lane; i < in; i += 128) {
-    const float4 gv = *reinterpret_cast<const float4*>(g + i), vv = *reinterpret_cast<const float4*>(v + i);
-    float d[4] = {dR(i, gv.x, vv.x), dR(i + 1, gv.y, vv.y), dR(i + 2, gv.z, vv.z), dR(i + 3, gv.w, vv.w)};
-    const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
+      for (int u = 0; u < kRbRows; ++u) {
+        if (u >= nr) break;
+        const float4 gv = *reinterpret_cast<const float4*>(G + (o0 + u) * in + i);
+        const float4 vv = *reinterpret_cast<const float4*>(V + (o0 + u) * in + i);
+        float d[4];
+        dr4(gv, vv, cf, tc, ro[u], d);
+        t[u] += (double)d[0] * vv.x + (double)d[1] * vv.y + (double)d[2] * vv.z + (double)d[3] * vv.w;
+      }
+    }
 #pragma unroll
-    for (int c = 0; c < 4; ++c) d[c] = s * (rows ? ro * (d[c] - vx[c] * t_over) : d[c]);
-    *reinterpret_cast<float4*>(g + i) = make_float4(d[0], d[1], d[2], d[3]);
+    for (int u = 0; u < kRbRows; ++u) {
+      const double w = warp_sum(t[u]);
+      if (lane == 0) red_t[warp][u] = w;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kRbRows; ++u) {
+      if (u >= nr) break;
+      double tt = 0.0;
+#pragma unroll
+      for (int k = 0; k < kRbWarps; ++k) tt += red_t[k][u];
+      t_over[u] = (float)(tt / rn2[o0 + u]);
+      if (tid == 0) dmr[o0 + u] = (float)(tt / sqrt(rn2[o0 + u]));
+    }
+  }
+  float acc[kRbRows][kMatMaxRank];
+#pragma unroll
+  for (int u = 0; u < kRbRows; ++u)
+#pragma unroll
+    for (int j = 0; j < kMatMaxRank; ++j) acc[u][j] = 0.f;
+  for (int64_t i = 4 * tid; i < in; i += 4 * kRbThreads) {
+    const float4 cf = cols ? *reinterpret_cast<const float4*>(cs + i) : one4;
+    const float4 tc = cols ? *reinterpret_cast<const float4*>(tcn + i) : one4;
+    float d[kRbRows][4];
+#pragma unroll
+    for (int u = 0; u < kRbRows; ++u) {
+      if (u >= nr) {
+        d[u][0] = d[u][1] = d[u][2] = d[u][3] = 0.f;
+        continue;
+      }
+      float* g = G + (o0 + u) * in + i;
+      const float4 gv = *reinterpret_cast<const float4*>(g);
+      const float4 vv = *reinterpret_cast<const float4*>(V + (o0 + u) * in + i);
+      dr4(gv, vv, cf, tc, ro[u], d[u]);
+      const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) d[u][c] = s * (rows ? ro[u] * (d[u][c] - vx[c] * t_over[u]) : d[u][c]);
+      *reinterpret_cast<float4*>(g) = make_float4(d[u][0], d[u][1], d[u][2], d[u][3]);
+    }
 #pragma unroll
     for (int j = 0; j < kMatMaxRank; ++j) {
       if (j >= r) break;
       const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
-      acc[j] = fmaf(d[0], q.x, fmaf(d[1], q.y, fmaf(d[2], q.z, fmaf(d[3], q.w, acc[j]))));
+#pragma unroll
+      for (int u = 0; u < kRbRows; ++u)
+        acc[u][j] = fmaf(d[u][0], q.x, fmaf(d[u][1], q.y, fmaf(d[u][2], q.z, fmaf(d[u][3], q.w, acc[u][j]))));
     }
   }
 #pragma unroll
-  for (int j = 0; j < kMatMaxRank; ++j) {
-    if (j >= r) break;
-    const float a = warp_sumf(acc[j]);
-    if (lane == 0) PG[o * r + j] = a;
+  for (int u = 0; u < kRbRows; ++u)
+#pragma unroll
+    for (int j = 0; j < kMatMaxRank; ++j) {
+      if (j >= r) break;
+      const float a = warp_sumf(acc[u][j]);
+      if (lane == 0) red_a[warp][u * kMatMaxRank + j] = a;
+    }
+  __syncthreads();
+  if (tid < kRbRows * kMatMaxRank) {
+    const int u = tid / kMatMaxRank, j = tid % kMatMaxRank;
+    if (u < nr && j < r) {
+      float a = 0.f;
+#pragma unroll
+      for (int k = 0; k < kRbWarps; ++k) a += red_a[k][tid];
+      PG[(o0 + u) * r + j] = a;
+    }
   }
 }
 
@@ -245,6 +336,7 @@ __global__ void __launch_bounds__(256) mat_da_kernel(const float* __restrict__ d
     for (int k = threadIdx.x; k < nb * r; k += blockDim.x) bs[k / r][k % r] = B[(ob + k / r) * r + k % r];
     __syncthreads();
     if (i < in) {
+#pragma unroll 4
       for (int q = 0; q < nb; ++q) {
         const float d = dD[(ob + q) * in + i];
 #pragma unroll
@@ -367,13 +459,16 @@ bool mat_alloc(Ctx* c, int64_t S, int64_t in, int64_t out, int r, bool bwd, MatB
   return true;
 }
 
-// Slices of rows for the column kernels: about two blocks of 256 columns per SM.
-int64_t col_rows_per(Ctx* c, int64_t out, int64_t in) {
-  const int64_t cb = (in + 255) / 256;
-  int64_t splits = (int64_t)(2 * c->sm_count) / cb;
-  splits = splits < 1 ? 1 : (splits > out ? out : splits);
-  return (out + splits - 1) / splits;
+// Slices of rows for the column kernels (blocks of `cols` columns): about four blocks per SM,
+// at least 16 rows a slice.
+int64_t col_rows_per(Ctx* c, int64_t out, int64_t in, int64_t cols) {
+  const int64_t cb = (in + cols - 1) / cols;
+  int64_t splits = (int64_t)(4 * c->sm_count) / cb;
+  splits = splits < 1 ? 1 : splits;
+  const int64_t rp = (out + splits - 1) / splits;
+  return rp < 16 ? 16 : rp;
 }
+constexpr int64_t kColBlockCols = 4 * kColThreads;
 
 // V, the row and column factors and W_eff (bf16 in b.wb; f32 into weff_f32 when not null).
 int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, MatBufs& b,
@@ -399,9 +494,9 @@ int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPla
   if (p.cols) {
     ProfScope prof_(c, "mat.cols");
     if (cudaMemsetAsync(b.csq, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
-    const int64_t rp = col_rows_per(c, out, in);
-    mat_colsum_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
-        b.V, nullptr, b.rs, out, in, rp, b.csq);
+    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
+    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
+                        kColThreads, 0, st>>>(b.V, nullptr, b.rs, out, in, rp, b.csq);
     if (check_launch("mat colsum", err)) return 1;
   }
   {
@@ -478,9 +573,9 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   if (p.cols) {
     ProfScope prof_(c, "mat.cols_bwd");
     if (cudaMemsetAsync(b.tc, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
-    const int64_t rp = col_rows_per(c, out, in);
-    mat_colsum_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
-        b.V, b.G, b.rs, out, in, rp, b.tc);
+    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
+    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
+                        kColThreads, 0, st>>>(b.V, b.G, b.rs, out, in, rp, b.tc);
     if (check_launch("mat colsum bwd", err)) return 1;
     mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, b.tc, p.mc, out, in, b.cs, b.tcn,
                                                                    p.rows ? g->dm_c : g->dm);
@@ -488,7 +583,7 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   }
   {
     ProfScope prof_(c, "mat.rows_bwd");
-    mat_rowbwd_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(
+    mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
         b.G, b.V, b.rs, b.rn2, b.cs, b.tcn, Q, out, in, r, ad->scale, p.rows ? 1 : 0, p.cols ? 1 : 0,
         p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB);
     if (check_launch("mat rows bwd", err)) return 1;
@@ -500,7 +595,7 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   }
   ProfScope prof_(c, "mat.dA");
   if (cudaMemsetAsync(g->dA, 0, sizeof(float) * (size_t)r * in, st) != cudaSuccess) return check_launch("memset", err);
-  const int64_t rp = col_rows_per(c, out, in);
+  const int64_t rp = col_rows_per(c, out, in, 256);
   mat_da_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
       b.G, ad->B, out, in, r, rp, g->dA);
   return check_launch("mat dA", err);

@@ -11,6 +11,13 @@ out = n (the weight is used transposed); the default is the forward y = x W^T + 
 --smem-dequant reads a quantized base as its codes, dequantized in shared memory.
 
     python sa3.cpp_b200/kernel_cases.py attention [--b 4 --h 24 --s 1088 --window -1] [--fwd-only]
+
+    python sa3.cpp_b200/kernel_cases.py mat --type bora [--m 1024 --n 1536 --k 1536 --rank 16]
+        [--qtype q8_0] [--reps 3] [--time]
+
+mat runs the forward and backward of a linear with a materialized adapter (W_eff built from the
+base and the low-rank update every call); --time prints each launch class with its algorithmic
+bytes or FLOPs per call.
 --time prints the CUDA-event time per launch (not to be used under a profiler)."""
 import argparse
 import os
@@ -110,6 +117,63 @@ def attention_case(a):
     ctx.close()
 
 
+def mat_case(a):
+    import torch
+    import sa3k
+    import gguf_blocks
+    torch.cuda.set_device(0)
+    ctx = sa3k.Context(0)
+    g = torch.Generator().manual_seed(0)
+    n, k, m, r = a.n, a.k, a.m, a.rank
+    W = torch.randn(n, k, generator=g) * 0.02
+    w = ctx.upload(gguf_blocks.encode(W.numpy(), a.qtype), a.qtype, k, n)
+    dev = torch.device("cuda", 0)
+    t = lambda *shape: torch.randn(*shape, device=dev) * 0.02
+    xs = a.type.endswith("-xs")
+    fam = a.type[:-3] if xs else a.type
+    p = dict(U=t(n, r), V=t(k, r), M=t(r, r)) if xs else dict(A=t(r, k), B=t(n, r))
+    grads = dict(dM=torch.empty(r, r, device=dev)) if xs else dict(dA=torch.empty(r, k, device=dev),
+                                                                     dB=torch.empty(n, r, device=dev))
+    if fam == "dora-rows":
+        p["m"], grads["dm"] = torch.ones(n, device=dev), torch.empty(n, device=dev)
+    elif fam == "dora-cols":
+        p["m"], grads["dm"] = torch.ones(k, device=dev), torch.empty(k, device=dev)
+    elif fam == "bora":
+        p["m_r"], p["m_c"] = torch.ones(n, device=dev), torch.ones(k, device=dev)
+        grads["dm_r"], grads["dm_c"] = torch.empty(n, device=dev), torch.empty(k, device=dev)
+    ad = ctx.mat_adapter(a.type, r, 1.0, **p)
+    x, dy = torch.randn(m, k, device=dev), torch.randn(m, n, device=dev)
+    y, dx = torch.empty(m, n, device=dev), torch.empty(m, k, device=dev)
+    run = lambda: ctx.linear_mat_fwd_bwd(w, ad, x, dy, y=y, dx=dx, **grads)
+    for _ in range(a.warmup):
+        run()
+    ctx.sync()
+    if a.time:
+        ctx.profile_enable(timing=1)
+    for _ in range(a.reps):
+        run()
+    ctx.sync()
+    if a.time:
+        E = n * k
+        code = {"q8_0": 1.0 + 4.0 / 32, "q4_k": 0.5 + 8.0 / 32}[a.qtype]
+        work = {"mat.build": (E * (code + 4), "B"), "mat.cols": (E * 4, "B"), "mat.weff": (E * 6, "B"),
+                "mat.transpose": (m * n * 6, "B"), "mat.cols_bwd": (E * 8, "B"), "mat.rows_bwd": (E * 12, "B"),
+                "mat.dA": (E * 4, "B"), "mat.fwd": (2.0 * m * n * k, "F"), "mat.dx": (2.0 * m * n * k, "F"),
+                "mat.dW": (2.0 * m * n * k, "F")}
+        total = 0.0
+        print(f"mat {a.type} {a.qtype} tokens {m}, in {k}, out {n}, rank {r}")
+        for name, (cnt, ms) in sorted(ctx.profile_read().items()):
+            us = ms / a.reps * 1e3
+            total += us
+            amt, kind = work.get(name, (0, ""))
+            rate = (f"{amt * cnt / a.reps / (us * 1e-6) / 1e9:8.0f} GB/s (algorithmic)" if kind == "B" else
+                    f"{amt * cnt / a.reps / (us * 1e-6) / 1e12:8.0f} TFLOP/s" if kind == "F" else "")
+            print(f"    {name:14s} {cnt // a.reps} launch(es) {us:8.1f} us  {rate}")
+        print(f"    total {total:.1f} us per call")
+    w.free()
+    ctx.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="case", required=True)
@@ -135,9 +199,21 @@ def main():
     at.add_argument("--warmup", type=int, default=2)
     at.add_argument("--reps", type=int, default=3)
     at.add_argument("--time", action="store_true")
+    mp = sub.add_parser("mat")
+    mp.add_argument("--type", default="bora")
+    mp.add_argument("--m", type=int, default=1024)
+    mp.add_argument("--n", type=int, default=1536)
+    mp.add_argument("--k", type=int, default=1536)
+    mp.add_argument("--rank", type=int, default=16)
+    mp.add_argument("--qtype", default="q8_0", choices=["q8_0", "q4_k"])
+    mp.add_argument("--warmup", type=int, default=2)
+    mp.add_argument("--reps", type=int, default=3)
+    mp.add_argument("--time", action="store_true")
     a = ap.parse_args()
     if a.case == "gemm":
         gemm_case(a)
+    elif a.case == "mat":
+        mat_case(a)
     else:
         attention_case(a)
 
