@@ -350,7 +350,12 @@ void sa3k_dit_free(sa3k_dit* dit);
 int sa3k_dit_set_tensor(sa3k_dit* dit, const char* name, int ggml_type, const void* host,
                         int64_t ne0, int64_t ne1, char* err, int err_len);
 
-/* Functional adapters ("lora" or "dora-rows", rank <= 16) on the named weights: any 2-D
+/* Adapters of any family of the reference on the named weights (rank <= 16): "lora" and
+ * "dora-rows" run functionally; "dora-cols", "bora" and every "-xs" form ("lora-xs",
+ * "dora-rows-xs", "dora-cols-xs", "bora-xs") through a materialized W_eff rebuilt every step
+ * (src/train_dit.h:90-164), the trainable tensors of each target laid out as
+ * sa3k_dit_adapter_layout reports; an -xs target needs its frozen bases from
+ * sa3k_dit_set_xs_bases before the first step.  Named weights: any 2-D
  * "*.weight" of the DiT, so the reference's `full` and `core` target scopes
  * (enumerate_train_lora_targets, src/train_lora.h:54-117) both fit; head adapters get their
  * gradient through x0, the context and gcond.  Allocates the flat adapter state [A | B | m] per target (order of `names`), zero; for
@@ -365,6 +370,16 @@ int sa3k_dit_init_adapters(sa3k_dit* dit, const char* adapter_type, int rank, fl
 int64_t sa3k_dit_adapter_size(const sa3k_dit* dit);
 int sa3k_dit_adapter_offsets(const sa3k_dit* dit, int idx, int64_t* offA, int64_t* offB,
                              int64_t* offM);
+/* Offsets of target idx's tensors in the flat state, -1 where the family has none: offs[0] A
+ * [rank][in], offs[1] B [out][rank], offs[2] the row magnitude [out] (dora-rows m, bora m_r),
+ * offs[3] the column magnitude [in] (dora-cols m, bora m_c), offs[4] M_xs [rank][rank]
+ * (TrainLoraParam, src/train_lora.h:24-33).  Magnitudes start at the base's row / column norms. */
+int sa3k_dit_adapter_layout(const sa3k_dit* dit, int idx, int64_t* offs);
+/* The frozen bases of an -xs target (host f32): U [out][rank], V [in][rank], the top-rank
+ * singular vectors of the base the reference computes or loads at init (init_train_lora_state,
+ * src/train_lora.h:223-251); the library takes them from the caller. */
+int sa3k_dit_set_xs_bases(sa3k_dit* dit, const char* name, const float* U, const float* V, char* err,
+                          int err_len);
 
 /* Device pointer of a flat buffer: 0 parameters, 1 accumulated gradients, 2 AdamW m, 3 AdamW v
  * (TrainLoraState / TrainLoraGradAccum / TrainLoopState of src/train_loop.h:21-39). */

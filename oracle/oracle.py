@@ -484,12 +484,40 @@ def expo_features(t, dim, min_f, max_f):
     return out
 
 
+def mat_weight_torch(W, p, adapter_type, scale):
+    """W_eff of a materialized family over torch tensors (differentiable), the definition of
+    src/train_lora.h:275-329: ggml's rms_norm(v, 1e-12) / sqrt(n) along rows (dora-rows, bora's
+    first step) or columns (dora-cols, bora's second step), scaled by the magnitudes."""
+    torch = _torch()
+    fam, xs = split_adapter_type(adapter_type)
+    delta = p["U"] @ p["M"] @ p["V"].t() if xs else p["B"] @ p["A"]
+    v = W + scale * delta
+    out, inn = W.shape
+
+    def rms(a, n):   # along the last dim, then / sqrt(n)
+        return a / torch.sqrt((a * a).mean(-1, keepdim=True) + MAT_EPS) / math.sqrt(n)
+
+    if fam == "lora":
+        return v
+    if fam == "dora-rows":
+        return rms(v, inn) * p["m"][:, None]
+    if fam == "dora-cols":
+        return (rms(v.t(), out) * p["m"][:, None]).t()
+    rowed = rms(v, inn) * p["m_r"][:, None]
+    return (rms(rowed.t(), out) * p["m_c"][:, None]).t()
+
+
 def lin(Wd, lora, name, x, bias=None):
-    """dit_lin over torch tensors: Wd[name] is W[out][in]; lora[name] = dict(A,B,m,bns,scale)."""
+    """dit_lin over torch tensors: Wd[name] is W[out][in]; lora[name] = dict(A,B,m,bns,scale), or
+    for a materialized family dict(type, scale, A, B | U, V, M, m | m_r, m_c): x W_eff^T, the
+    weight override of src/train_dit.h:159-164."""
     torch = _torch()
     W = Wd[name]
-    y = torch.matmul(x, W.t())
     p = lora.get(name) if lora else None
+    if p is not None and p.get("type"):
+        y = torch.matmul(x, mat_weight_torch(W, p, p["type"], p["scale"]).t())
+        return y + bias if bias is not None else y
+    y = torch.matmul(x, W.t())
     if p is not None:
         A, B, s = p["A"], p["B"], p["scale"]
         y = y + s * torch.matmul(torch.matmul(x, A.t()), B.t())

@@ -26,6 +26,7 @@
 #include "gguf_io.h"
 #include "linear.h"
 #include "lora_kernels.h"
+#include "materialize.h"
 
 #include <algorithm>
 #include <cmath>
@@ -59,6 +60,14 @@ struct DitTarget {
   __nv_bfloat16 *ut = nullptr, *dz = nullptr, *dut = nullptr, *cb = nullptr;
   float *dg = nullptr, *c3 = nullptr;
   const __nv_bfloat16* x_bf = nullptr;
+  // materialized families (dora-cols, bora, every -xs form): W_eff built once per step, the
+  // forward and dX GEMMs on it, the weight gradient per backward (outside the functional
+  // adapters' grouped preparation and gradient passes).  offMc: the bora column magnitude;
+  // offX: M_xs; U [out][rank] / Vb [in][rank]: the frozen -xs bases (device)
+  bool mat = false;
+  MatTarget mt;
+  int64_t offMc = -1, offX = -1;
+  float *U = nullptr, *Vb = nullptr;
 };
 
 struct DitBlockAct {
@@ -92,6 +101,11 @@ struct DitModel {
   std::vector<void*> owned;            // device allocations of this model
   // adapters
   bool dora = false;
+  bool mat = false;                    // a materialized family (every target is a DitTarget::mat)
+  std::string adapter_type = "lora";
+  float* mat_G = nullptr;              // [max out*in] f32 weight-gradient scratch (materialized)
+  __nv_bfloat16* mat_dzt = nullptr;    // [max out][mat_ldt] bf16 transposed output gradient
+  int64_t mat_ldt = 0;
   int rank = 0;
   float alpha = 1.f, s = 1.f;
   std::vector<DitTarget> tg;
@@ -257,7 +271,7 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
   std::vector<PrepDesc> descs;
   std::vector<R16Job> prep, grads;
   for (DitTarget& t : m.tg) {
-    if (t.inert) continue;
+    if (t.inert || t.mat) continue;
     const AdapterPrep& p = t.prep;
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
@@ -304,7 +318,7 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
   // every DoRA base needs its bf16 copy for the grouped P and dA terms (else the per-adapter
   // GEMMs over the quantized codes run instead)
   bool all_bf16 = true;
-  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (t.inert || !t.prep.dora() || t.w->bf16);
+  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (t.inert || t.mat || !t.prep.dora() || t.w->bf16);
   r16_group_free(m.r16_prep);
   r16_group_free(m.r16_grads);
   if (!all_bf16 || grads.empty()) return 0;
@@ -392,7 +406,19 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       t.ut = h(16 * t.ut_ld);
       t.dz = h(t.rows * t.out); t.dg = f(t.out); t.dut = h(16 * t.ut_ld);
       t.cb = m.dora ? h(16 * t.out) : nullptr;
-      t.c3 = m.c3_all ? m.c3_all + 256 * (int64_t)t.act : nullptr;
+      t.c3 = m.c3_all && t.act >= 0 ? m.c3_all + 256 * (int64_t)t.act : nullptr;
+    }
+    if (m.mat) {   // weight-gradient scratch of the materialized targets, reused target by target
+      int64_t wn = 0, mo = 0, mr = 0;
+      for (const DitTarget& t : m.tg) {
+        if (t.inert) continue;
+        wn = std::max<int64_t>(wn, t.in * t.out);
+        mo = std::max<int64_t>(mo, t.out);
+        mr = std::max<int64_t>(mr, t.rows);
+      }
+      m.mat_ldt = (mr + 7) / 8 * 8;
+      m.mat_G = f(wn);
+      m.mat_dzt = h(mo * m.mat_ldt);
     }
     if (pass == 0) {
       m.arena_bytes = off;
@@ -410,6 +436,18 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
 // ------------------------------------------------------------------ linear helpers
 static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __nv_bfloat16* x,
                    int64_t M, float* y, __nv_bfloat16* y_bf, std::string& err) {
+  if (t && t->mat) {
+    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    GemmDesc g;   // y = x W_eff^T + bias
+    g.M = (int)M; g.N = (int)t->out; g.K = (int)t->in;
+    g.a = x; g.lda = t->in;
+    g.bsrc = kB_BF16_KMAJOR; g.b = t->mt.wb; g.ldb = t->in;
+    g.col_bias = bias;
+    g.out = y; g.ldo = t->out;
+    g.out_bf = y_bf; g.ldo_bf = t->out;
+    g.name = "linear.fwd";
+    return gemm(m.c, g, err);
+  }
   LinearFwd f;
   f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_bf = x; f.M = M; f.y = y; f.y_bf = y_bf;
   if (t) {
@@ -423,6 +461,22 @@ static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float
 static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
                    const float* y, const float* dy, int64_t M, float* dx, int dx_acc, __nv_bfloat16* dx_bf,
                    std::string& err) {
+  if (t && t->mat) {
+    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    // dz = bf16(dy), or already written to m.dz by the fused producer of dy
+    if (dy && k_cvt_bf16(m.c, dy, M * t->out, m.dz, err)) return 1;
+    if (dx || dx_bf) {
+      GemmDesc g;   // dx = dz W_eff
+      g.M = (int)M; g.N = (int)t->in; g.K = (int)t->out;
+      g.a = m.dz; g.lda = t->out;
+      g.bsrc = kB_BF16_MNMAJOR; g.b = t->mt.wb; g.ldb = t->in;
+      g.out = dx; g.ldo = t->in; g.accumulate = dx_acc;
+      g.out_bf = dx_bf; g.ldo_bf = t->in;
+      g.name = "linear.dx";
+      if (gemm(m.c, g, err)) return 1;
+    }
+    return mat_target_backward(m.c, t->mt, m.dz, M, x, m.mat_G, m.mat_dzt, m.mat_ldt, err);
+  }
   LinearBwd b;
   b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;
   b.dz_ready = dy == nullptr;
@@ -484,8 +538,10 @@ static int mlp_silu_bwd(DitModel& m, const std::string& pfx, bool bias, const __
 }
 
 // where the backward of linear `t` (null: a linear without adapter) expects its dz / dg
-static __nv_bfloat16* dz_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dz : m.dz; }
-static float* dg_of(DitModel& m, const DitTarget* t) { return t && m.r16_grads.table ? t->dg : m.dg; }
+static __nv_bfloat16* dz_of(DitModel& m, const DitTarget* t) {
+  return t && !t->mat && m.r16_grads.table ? t->dz : m.dz;
+}
+static float* dg_of(DitModel& m, const DitTarget* t) { return t && !t->mat && m.r16_grads.table ? t->dg : m.dg; }
 
 // self-attention of block `a` over the prepared [q | k | v (| qd | kd)] rows: softmax stream 0
 // (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] bf16
@@ -540,6 +596,9 @@ static int dit_step(DitModel& m, std::string& err) {
     }
     if (k_dora_norm_all(c, m.prep_desc, nt, m.max_out, err)) return 1;
   }
+  // materialized families: W_eff of every target from this step's parameters
+  for (DitTarget& t : m.tg)
+    if (t.mat && !t.inert && mat_target_build(c, t.mt, err)) return 1;
 
   // ---------------- head (src/dit.h:286-310)
   if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
@@ -1083,11 +1142,19 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
   DitModel& m = d->m;
   cudaSetDevice(m.c->device);
   const std::string at(adapter_type);
-  if (at != "lora" && at != "dora-rows") return dfail(err, err_len, "adapter type must be lora or dora-rows");
+  // lora / dora-rows run functionally; the other families through a materialized W_eff
+  // (src/train_dit.h:90-164)
+  const bool xs = at.size() > 3 && at.compare(at.size() - 3, 3, "-xs") == 0;
+  const std::string fam = xs ? at.substr(0, at.size() - 3) : at;
+  if (fam != "lora" && fam != "dora-rows" && fam != "dora-cols" && fam != "bora")
+    return dfail(err, err_len, "unknown adapter type " + at);
   if (rank < 1 || rank > 16) return dfail(err, err_len, "rank must be 1..16");
   if (!m.tg.empty()) return dfail(err, err_len, "adapters already initialised");
   ++m.gen;
-  m.dora = at == "dora-rows";
+  m.adapter_type = at;
+  m.mat = xs || fam == "dora-cols" || fam == "bora";
+  const bool mrows = fam == "dora-rows" || fam == "bora", mcols = fam == "dora-cols" || fam == "bora";
+  m.dora = !m.mat && at == "dora-rows";
   m.rank = rank;
   m.alpha = alpha;
   m.s = alpha / (float)rank;
@@ -1110,10 +1177,20 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
       t.out = ht->second.second;
     }
     if (!t.inert && !t.w) return dfail(err, err_len, "adapter target has no device weight: " + t.name);
-    if (!t.inert) t.act = m.n_active++;
-    t.offA = off; off += (int64_t)rank * t.in;
-    t.offB = off; off += t.out * rank;
-    if (m.dora) { t.offM = off; off += t.out; }
+    t.mat = m.mat;
+    if (!t.inert && !t.mat) t.act = m.n_active++;
+    if (m.mat && xs) {   // trainable M_xs only; A / B absent (offA = offB = -1)
+      t.offA = t.offB = -1;
+      t.offX = off; off += (int64_t)rank * rank;
+    } else {
+      t.offA = off; off += (int64_t)rank * t.in;
+      t.offB = off; off += t.out * rank;
+    }
+    if (m.dora || (m.mat && mrows)) { t.offM = off; off += t.out; }
+    if (m.mat && mcols) {
+      if (mrows) { t.offMc = off; off += t.in; }    // bora: m_r [out] at offM, m_c [in] at offMc
+      else { t.offM = off; off += t.in; }          // dora-cols: m [in] at offM
+    }
     m.tix[t.name] = (int)m.tg.size();
     m.tg.push_back(t);
   }
@@ -1122,6 +1199,55 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     *b = static_cast<float*>(dmalloc(m, (size_t)off * 4, e));
     if (!*b) return dfail(err, err_len, e);
     cudaMemsetAsync(*b, 0, (size_t)off * 4, m.c->stream);
+  }
+  if (m.mat) {
+    for (DitTarget& t : m.tg) {
+      // magnitudes start at the base's row / column norms (train_row_norms / train_col_norms,
+      // src/train_lora.h:141-190, 262-269)
+      const int64_t om = t.offM, oc = mcols ? (mrows ? t.offMc : t.offM) : -1;
+      if (t.w) {
+        if (mrows && weight_row_norms(m.c, t.w, 1e-12f, nullptr, m.p + om, e)) return dfail(err, err_len, e);
+        if (mcols && mat_col_norms(m.c, t.w, m.p + oc, e)) return dfail(err, err_len, e);
+      } else if (mrows || mcols) {   // a host-only weight: the same f64 sums on the host
+        const std::vector<float>& hw = m.host_w[t.name];
+        std::vector<float> rn((size_t)t.out), cn((size_t)t.in);
+        std::vector<double> ca((size_t)t.in, 0.0);
+        for (int64_t o = 0; o < t.out; ++o) {
+          double acc = 0.0;
+          for (int64_t i = 0; i < t.in; ++i) {
+            const double v = hw[(size_t)(o * t.in + i)];
+            acc += v * v;
+            ca[(size_t)i] += v * v;
+          }
+          rn[(size_t)o] = (float)std::sqrt(acc);
+        }
+        for (int64_t i = 0; i < t.in; ++i) cn[(size_t)i] = (float)std::sqrt(ca[(size_t)i]);
+        if ((mrows && cudaMemcpy(m.p + om, rn.data(), 4 * rn.size(), cudaMemcpyHostToDevice) != cudaSuccess) ||
+            (mcols && cudaMemcpy(m.p + oc, cn.data(), 4 * cn.size(), cudaMemcpyHostToDevice) != cudaSuccess))
+          return dfail(err, err_len, "magnitude init copy failed");
+      }
+      if (t.inert) continue;
+      MatTarget& mt = t.mt;
+      mt.xs = xs; mt.rows = mrows; mt.cols = mcols;
+      mt.rank = rank; mt.s = m.s; mt.w = t.w; mt.in = t.in; mt.out = t.out;
+      if (xs) {
+        t.U = static_cast<float*>(dmalloc(m, 4 * (size_t)t.out * rank, e));
+        t.Vb = static_cast<float*>(dmalloc(m, 4 * (size_t)t.in * rank, e));
+        if (!t.U || !t.Vb) return dfail(err, err_len, e);
+        cudaMemsetAsync(t.U, 0, 4 * (size_t)t.out * rank, m.c->stream);
+        cudaMemsetAsync(t.Vb, 0, 4 * (size_t)t.in * rank, m.c->stream);
+        mt.U = t.U; mt.Vb = t.Vb; mt.M = m.p + t.offX; mt.dM = m.g + t.offX;
+      } else {
+        mt.A = m.p + t.offA; mt.B = m.p + t.offB; mt.dA = m.g + t.offA; mt.dB = m.g + t.offB;
+      }
+      if (mrows) { mt.mr = m.p + t.offM; mt.dmr = m.g + t.offM; }
+      if (mcols) { mt.mc = m.p + oc; mt.dmc = m.g + oc; }
+      void* mem = dmalloc(m, mat_target_bytes(t.in, t.out, rank), e);
+      if (!mem) return dfail(err, err_len, e);
+      mat_target_bind(mt, mem);
+    }
+    if (cudaStreamSynchronize(m.c->stream) != cudaSuccess) return dfail(err, err_len, "adapter init failed");
+    return 0;
   }
   size_t prep_bytes = 256;
   for (DitTarget& t : m.tg)
@@ -1189,6 +1315,33 @@ int sa3k_dit_adapter_offsets(const sa3k_dit* d, int idx, int64_t* offA, int64_t*
   if (offA) *offA = t.offA;
   if (offB) *offB = t.offB;
   if (offM) *offM = t.offM;
+  return 0;
+}
+
+int sa3k_dit_adapter_layout(const sa3k_dit* d, int idx, int64_t* offs) {
+  if (!d || !offs || idx < 0 || idx >= (int)d->m.tg.size()) return 1;
+  const DitTarget& t = d->m.tg[(size_t)idx];
+  const bool bora = t.offMc >= 0;
+  const bool cols = d->m.mat && (bora || d->m.adapter_type.rfind("dora-cols", 0) == 0);
+  offs[0] = t.offA;
+  offs[1] = t.offB;
+  offs[2] = cols && !bora ? -1 : t.offM;   // row magnitude [out]
+  offs[3] = bora ? t.offMc : (cols ? t.offM : -1);   // column magnitude [in]
+  offs[4] = t.offX;
+  return 0;
+}
+
+int sa3k_dit_set_xs_bases(sa3k_dit* d, const char* name, const float* U, const float* V, char* err, int err_len) {
+  if (!d || !name || !U || !V) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  auto it = m.tix.find(name);
+  if (it == m.tix.end()) return dfail(err, err_len, std::string("no adapter target ") + name);
+  DitTarget& t = m.tg[(size_t)it->second];
+  if (!t.U) return dfail(err, err_len, "the adapters are not of an -xs family (or the target is inert)");
+  cudaSetDevice(m.c->device);
+  if (cudaMemcpy(t.U, U, 4 * (size_t)t.out * m.rank, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(t.Vb, V, 4 * (size_t)t.in * m.rank, cudaMemcpyHostToDevice) != cudaSuccess)
+    return dfail(err, err_len, "basis copy failed");
   return 0;
 }
 
@@ -1299,9 +1452,13 @@ static int store_flat(DitModel& m, float* dev, const std::vector<float>& host, s
   return 0;
 }
 
-static std::string adapter_type_of(const DitModel& m) { return m.dora ? "dora-rows" : "lora"; }
+static std::string adapter_type_of(const DitModel& m) { return m.adapter_type; }
 
 static int write_adapter_file(DitModel& m, const std::string& path, std::string& err) {
+  if (m.mat) {
+    err = "adapter files are written for lora and dora-rows adapters only (not " + m.adapter_type + ")";
+    return 1;
+  }
   std::vector<float> p;
   if (fetch_flat(m, m.p, p, err)) return 1;
   std::vector<AdapterTargetView> v;
@@ -1323,6 +1480,10 @@ static int write_adapter_file(DitModel& m, const std::string& path, std::string&
 // train_restore_adapter_values (src/train_resume.h:104-148): same type, rank and alpha, the same
 // set of targets, every tensor of the expected size.
 static int read_adapter_file(const DitModel& m, const std::string& path, std::vector<float>& p, std::string& err) {
+  if (m.mat) {
+    err = "adapter files are read for lora and dora-rows adapters only (not " + m.adapter_type + ")";
+    return 1;
+  }
   GgufFile f;
   if (!f.open(path, err)) return 1;
   const GgufValue* ty = f.find("lora.adapter_type");

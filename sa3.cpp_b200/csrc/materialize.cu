@@ -18,6 +18,7 @@
 // twice); the three GEMMs carry the FLOPs.
 #include "../../include/sa3k.h"
 #include "linear.h"
+#include "materialize.h"
 #include "lora_kernels.h"
 #include "sa3k_common.cuh"
 #include "sa3k_internal.h"
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(kColThreads) mat_colsum_kernel(const float* __
 // With tc (the backward): cfac = cs, tcn[i] = tc / cn^2 and dmc[i] = tc / cn.
 __global__ void mat_colfac_kernel(const double* __restrict__ csq, const double* __restrict__ tc,
                                   const float* __restrict__ mc, int64_t out, int64_t in, float* __restrict__ cs,
-                                  float* __restrict__ tcn, float* __restrict__ dmc) {
+                                  float* __restrict__ tcn, float* __restrict__ dmc, int acc) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= in) return;
   if (!mc) {
@@ -158,7 +159,7 @@ __global__ void mat_colfac_kernel(const double* __restrict__ csq, const double* 
   cs[i] = (float)((double)mc[i] / n);
   if (tc) {
     tcn[i] = (float)(tc[i] / n2);
-    if (dmc) dmc[i] = (float)(tc[i] / n);
+    if (dmc) dmc[i] = (float)(tc[i] / n) + (acc ? dmc[i] : 0.f);
   }
 }
 
@@ -212,7 +213,8 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
                                                                 const float* __restrict__ tcn,
                                                                 const float* __restrict__ Q, int64_t out, int64_t in,
                                                                 int r, float s, int rows, int cols,
-                                                                float* __restrict__ dmr, float* __restrict__ PG) {
+                                                                float* __restrict__ dmr, float* __restrict__ PG,
+                                                                int acc_pg, int acc_dm) {
   __shared__ double red_t[kRbWarps][kRbRows];
   __shared__ float red_a[kRbWarps][kRbRows * kMatMaxRank];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
 #pragma unroll
       for (int k = 0; k < kRbWarps; ++k) tt += red_t[k][u];
       t_over[u] = (float)(tt / rn2[o0 + u]);
-      if (tid == 0) dmr[o0 + u] = (float)(tt / sqrt(rn2[o0 + u]));
+      if (tid == 0) dmr[o0 + u] = (float)(tt / sqrt(rn2[o0 + u])) + (acc_dm ? dmr[o0 + u] : 0.f);
     }
   }
   float acc[kRbRows][kMatMaxRank];
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
       float a = 0.f;
 #pragma unroll
       for (int k = 0; k < kRbWarps; ++k) a += red_a[k][tid];
-      PG[(o0 + u) * r + j] = a;
+      PG[(o0 + u) * r + j] = a + (acc_pg ? PG[(o0 + u) * r + j] : 0.f);
     }
   }
 }
@@ -358,7 +360,7 @@ __global__ void __launch_bounds__(256) mat_da_kernel(const float* __restrict__ d
 
 // dM[a][b] = sum_o U[o][a] PG[o][b] (PG = dD V), one block per (a, b).
 __global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __restrict__ PG, int64_t out, int r,
-                                 float* __restrict__ dM) {
+                                 float* __restrict__ dM, int acc_out) {
   const int a = blockIdx.x / r, b = blockIdx.x % r;
   float acc = 0.f;
   for (int64_t o = threadIdx.x; o < out; o += blockDim.x) acc = fmaf(U[o * r + a], PG[o * r + b], acc);
@@ -369,8 +371,36 @@ __global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __res
   if (threadIdx.x < 32) {
     float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
     v = warp_sumf(v);
-    if (threadIdx.x == 0) dM[blockIdx.x] = v;
+    if (threadIdx.x == 0) dM[blockIdx.x] = v + (acc_out ? dM[blockIdx.x] : 0.f);
   }
+}
+
+// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld], 32 x 32 tiles.
+__global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t S, int64_t out,
+                                           __nv_bfloat16* __restrict__ dst, int64_t ld) {
+  __shared__ __nv_bfloat16 t[32][34];
+  const int64_t s0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t s = s0 + k, o = o0 + threadIdx.x;
+    t[k][threadIdx.x] = (s < S && o < out) ? src[s * out + o] : __float2bfloat16_rn(0.f);
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int64_t o = o0 + k, s = s0 + threadIdx.x;
+    if (o < out && s < S) dst[o * ld + s] = t[threadIdx.x][k];
+  }
+}
+
+// nrm[i] = sqrt(sum_o W[o][i]^2), one thread per column, f64 sums.
+__global__ void mat_col_norms_kernel(const Weight w, float* __restrict__ nrm) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= w.in) return;
+  double a = 0.0;
+  for (int64_t o = 0; o < w.out; ++o) {
+    const double v = (double)wval(w, o, i);
+    a += v * v;
+  }
+  nrm[i] = (float)sqrt(a);
 }
 
 struct MatPlan {
@@ -502,7 +532,7 @@ int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPla
   {
     ProfScope prof_(c, "mat.weff");
     mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, nullptr, p.mc, out, in, b.cs, nullptr,
-                                                                   nullptr);
+                                                                   nullptr, 0);
     if (check_launch("mat colfac", err)) return 1;
     mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(b.V, b.rs, b.cs, out, in, b.wb, weff_f32);
     if (check_launch("mat weff", err)) return 1;
@@ -578,19 +608,19 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
                         kColThreads, 0, st>>>(b.V, b.G, b.rs, out, in, rp, b.tc);
     if (check_launch("mat colsum bwd", err)) return 1;
     mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, b.tc, p.mc, out, in, b.cs, b.tcn,
-                                                                   p.rows ? g->dm_c : g->dm);
+                                                                   p.rows ? g->dm_c : g->dm, 0);
     if (check_launch("mat colfac bwd", err)) return 1;
   }
   {
     ProfScope prof_(c, "mat.rows_bwd");
     mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
         b.G, b.V, b.rs, b.rn2, b.cs, b.tcn, Q, out, in, r, ad->scale, p.rows ? 1 : 0, p.cols ? 1 : 0,
-        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB);
+        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB, 0, 0);
     if (check_launch("mat rows bwd", err)) return 1;
   }
   if (p.xs) {
     ProfScope prof_(c, "mat.dM");
-    mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(ad->U, b.PG, out, r, g->dM);
+    mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(ad->U, b.PG, out, r, g->dM, 0);
     return check_launch("mat dM", err);
   }
   ProfScope prof_(c, "mat.dA");
@@ -610,6 +640,131 @@ int mfail(char* err, int len, const std::string& msg) {
 }
 
 }  // namespace
+
+size_t mat_target_bytes(int64_t in, int64_t out, int rank) {
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t wn = (size_t)(in * out);
+  return al(4 * wn) + al(2 * wn) + 2 * al(4 * (size_t)out * rank) + al(4 * (size_t)rank * in) + al(4 * out) +
+         2 * al(4 * in) + al(8 * out) + 2 * al(8 * in);
+}
+
+void mat_target_bind(MatTarget& t, void* mem) {
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  uint8_t* p = static_cast<uint8_t*>(mem);
+  auto take = [&](size_t bytes) { uint8_t* q = p; p += al(bytes); return q; };
+  const size_t wn = (size_t)(t.in * t.out);
+  t.V = reinterpret_cast<float*>(take(4 * wn));
+  t.wb = reinterpret_cast<__nv_bfloat16*>(take(2 * wn));
+  t.P = reinterpret_cast<float*>(take(4 * (size_t)t.out * t.rank));
+  t.PG = reinterpret_cast<float*>(take(4 * (size_t)t.out * t.rank));
+  t.Q = reinterpret_cast<float*>(take(4 * (size_t)t.rank * t.in));
+  t.rs = reinterpret_cast<float*>(take(4 * t.out));
+  t.cs = reinterpret_cast<float*>(take(4 * t.in));
+  t.tcn = reinterpret_cast<float*>(take(4 * t.in));
+  t.rn2 = reinterpret_cast<double*>(take(8 * t.out));
+  t.csq = reinterpret_cast<double*>(take(8 * t.in));
+  t.tc = reinterpret_cast<double*>(take(8 * t.in));
+}
+
+int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
+  const int64_t in = t.in, out = t.out;
+  const int r = t.rank;
+  const cudaStream_t st = c->stream;
+  const float* P = t.B;
+  const float* Q = t.A;
+  if (t.xs) {
+    if (!t.U || !t.Vb) {
+      err = "the -xs adapter has no U / V bases";
+      return 1;
+    }
+    ProfScope prof_(c, "mat.xs_prep");
+    mat_xs_prep_kernel<<<(unsigned)(2 * c->sm_count), 256, 0, st>>>(t.U, t.M, t.Vb, out, in, r, t.P, t.Q);
+    if (check_launch("mat xs prep", err)) return 1;
+    P = t.P;
+    Q = t.Q;
+  }
+  {
+    ProfScope prof_(c, "mat.build");
+    mat_build_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(*t.w, P, Q, r, t.s,
+                                                                                  t.rows ? t.mr : nullptr, t.V,
+                                                                                  t.rn2, t.rs);
+    if (check_launch("mat build", err)) return 1;
+  }
+  if (t.cols) {
+    ProfScope prof_(c, "mat.cols");
+    if (cudaMemsetAsync(t.csq, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
+    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
+    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
+                        kColThreads, 0, st>>>(t.V, nullptr, t.rs, out, in, rp, t.csq);
+    if (check_launch("mat colsum", err)) return 1;
+  }
+  ProfScope prof_(c, "mat.weff");
+  mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(t.csq, nullptr, t.cols ? t.mc : nullptr, out, in,
+                                                                 t.cs, nullptr, nullptr, 0);
+  if (check_launch("mat colfac", err)) return 1;
+  mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(t.V, t.rs, t.cs, out, in, t.wb, nullptr);
+  return check_launch("mat weff", err);
+}
+
+int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M, const __nv_bfloat16* x,
+                        float* G, __nv_bfloat16* dzt, int64_t ldt, std::string& err) {
+  const int64_t in = t.in, out = t.out;
+  const int r = t.rank;
+  const cudaStream_t st = c->stream;
+  if (ldt < M || ldt % 8) {
+    err = "mat backward: transposed gradient pitch";
+    return 1;
+  }
+  {
+    ProfScope prof_(c, "mat.transpose");
+    transpose_bf16_bf16_kernel<<<dim3((unsigned)((M + 31) / 32), (unsigned)((out + 31) / 32)), dim3(32, 8), 0, st>>>(
+        dz, M, out, dzt, ldt);
+    if (check_launch("mat transpose", err)) return 1;
+  }
+  {
+    GemmDesc d;   // G = dz^T x  [out][in], K = token rows
+    d.M = (int)out; d.N = (int)in; d.K = (int)M;
+    d.a = dzt; d.lda = ldt;
+    d.bsrc = kB_BF16_MNMAJOR; d.b = x; d.ldb = in;
+    d.out = G; d.ldo = in;
+    d.name = "mat.dW";
+    if (gemm(c, d, err)) return 1;
+  }
+  if (t.cols) {
+    ProfScope prof_(c, "mat.cols_bwd");
+    if (cudaMemsetAsync(t.tc, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
+    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
+    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
+                        kColThreads, 0, st>>>(t.V, G, t.rs, out, in, rp, t.tc);
+    if (check_launch("mat colsum bwd", err)) return 1;
+    mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(t.csq, t.tc, t.mc, out, in, t.cs, t.tcn, t.dmc, 1);
+    if (check_launch("mat colfac bwd", err)) return 1;
+  }
+  {
+    ProfScope prof_(c, "mat.rows_bwd");
+    mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
+        G, t.V, t.rs, t.rn2, t.cs, t.tcn, t.xs ? t.Q : t.A, out, in, r, t.s, t.rows ? 1 : 0, t.cols ? 1 : 0,
+        t.rows ? t.dmr : nullptr, t.xs ? t.PG : t.dB, t.xs ? 0 : 1, 1);
+    if (check_launch("mat rows bwd", err)) return 1;
+  }
+  if (t.xs) {
+    ProfScope prof_(c, "mat.dM");
+    mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(t.U, t.PG, out, r, t.dM, 1);
+    return check_launch("mat dM", err);
+  }
+  ProfScope prof_(c, "mat.dA");
+  const int64_t rp = col_rows_per(c, out, in, 256);
+  mat_da_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
+      G, t.B, out, in, r, rp, t.dA);
+  return check_launch("mat dA", err);
+}
+
+int mat_col_norms(Ctx* c, const Weight* w, float* nrm, std::string& err) {
+  ProfScope prof_(c, "col norms");
+  mat_col_norms_kernel<<<(unsigned)((w->in + 255) / 256), 256, 0, c->stream>>>(*w, nrm);
+  return check_launch("col norms", err);
+}
+
 }  // namespace sa3k
 
 using namespace sa3k;

@@ -30,7 +30,7 @@ ABI_SYMBOLS = (
     "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
     "sa3k_gguf_get_u64_array", "sa3k_gguf_get_f32", "sa3k_lora_chain_build", "sa3k_lora_chain_free",
     "sa3k_lora_chain_info", "sa3k_linear_fwd_chain", "sa3k_mat_effective_weight", "sa3k_linear_mat_fwd",
-    "sa3k_linear_mat_fwd_bwd",
+    "sa3k_linear_mat_fwd_bwd", "sa3k_dit_adapter_layout", "sa3k_dit_set_xs_bases",
 )
 OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
@@ -148,6 +148,8 @@ def lib():
         L.sa3k_dit_adapter_size.argtypes = [P]
         L.sa3k_dit_adapter_offsets.argtypes = [P, I, ctypes.POINTER(I64), ctypes.POINTER(I64), ctypes.POINTER(I64)]
         L.sa3k_dit_adapter_buffer.argtypes = [P, I, ctypes.POINTER(P), E, I]
+        L.sa3k_dit_adapter_layout.argtypes = [P, I, ctypes.POINTER(I64)]
+        L.sa3k_dit_set_xs_bases.argtypes = [P, ctypes.c_char_p, P, P, E, I]
         L.sa3k_dit_adapter_copy.argtypes = [P, I, P, I64, I64, I, E, I]
         L.sa3k_dit_zero_grads.argtypes = [P, E, I]
         L.sa3k_dit_forward_backward.argtypes = [P, I, I, I, P, P, P, P, P, P, E, I]
@@ -487,6 +489,20 @@ class Dit:
         if lib().sa3k_dit_adapter_offsets(self._h, idx, ctypes.byref(a), ctypes.byref(b), ctypes.byref(m)):
             raise Sa3kError("bad target index")
         return a.value, b.value, m.value
+
+    def layout(self, idx):
+        """(A, B, row magnitude, column magnitude, M_xs) offsets of target idx, -1 where absent."""
+        offs = (ctypes.c_int64 * 5)()
+        if lib().sa3k_dit_adapter_layout(self._h, idx, offs):
+            raise Sa3kError("bad target index")
+        return tuple(int(v) for v in offs)
+
+    def set_xs_bases(self, name, U, V):
+        import numpy as np
+        U = np.ascontiguousarray(U, np.float32)
+        V = np.ascontiguousarray(V, np.float32)
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_dit_set_xs_bases(self._h, name.encode(), _ptr(U), _ptr(V), err, 512), err)
 
     def copy(self, which, buf, offset=0, count=None, to_model=True):
         """which: 0 params, 1 grads, 2 AdamW m, 3 AdamW v; buf: numpy float32 (host) or torch tensor."""

@@ -140,3 +140,18 @@ def test_functional_equals_materialized(adapter_type):
     assert np.abs(yf - ym).max() < 1e-10
     for k in ("dx", "dA", "dB") + (("dm",) if dora else ()):
         assert np.abs(gf[k] - gm[k]).max() < 1e-9, k
+
+
+@pytest.mark.parametrize("adapter_type", TYPES)
+def test_torch_weight_equals_numpy_weight(adapter_type):
+    """The oracle's two forms of W_eff (torch, used inside the DiT restatement; numpy, used by the
+    linear-level tests) agree."""
+    import torch
+    rng = np.random.default_rng(3)
+    out, inn, r, s = 6, 10, 2, 0.7
+    W = rng.standard_normal((out, inn))
+    p = _params(rng, out, inn, r, adapter_type)
+    ref, _ = oracle.mat_effective_weight(W, p, adapter_type, s)
+    tp = {k: torch.tensor(v, dtype=torch.float64) for k, v in p.items()}
+    got = oracle.mat_weight_torch(torch.tensor(W), tp, adapter_type, s).numpy()
+    assert np.abs(got - ref).max() < 1e-12
