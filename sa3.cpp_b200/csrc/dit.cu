@@ -1454,23 +1454,67 @@ static int store_flat(DitModel& m, float* dev, const std::vector<float>& host, s
 
 static std::string adapter_type_of(const DitModel& m) { return m.adapter_type; }
 
-static int write_adapter_file(DitModel& m, const std::string& path, std::string& err) {
-  if (m.mat) {
-    err = "adapter files are written for lora and dora-rows adapters only (not " + m.adapter_type + ")";
-    return 1;
+// The trainable tensors of one target in the flat state, named and ordered as the reference's
+// adapter and trainer-state files hold them (src/train_checkpoint.h:68-99, src/train_resume.h:
+// 319-331): lora_A, lora_B, M_xs, magnitude (dora-rows [out] / dora-cols [in]), magnitude_r,
+// magnitude_c.
+struct Part {
+  const char* kind;
+  int64_t off, count;
+};
+static std::vector<Part> target_parts(const DitModel& m, const DitTarget& t) {
+  std::vector<Part> v;
+  if (t.offA >= 0) v.push_back({"lora_A", t.offA, (int64_t)m.rank * t.in});
+  if (t.offB >= 0) v.push_back({"lora_B", t.offB, t.out * m.rank});
+  if (t.offX >= 0) v.push_back({"M_xs", t.offX, (int64_t)m.rank * m.rank});
+  const bool cols = m.adapter_type.rfind("dora-cols", 0) == 0;
+  if (t.offMc >= 0) {
+    v.push_back({"magnitude_r", t.offM, t.out});
+    v.push_back({"magnitude_c", t.offMc, t.in});
+  } else if (t.offM >= 0) {
+    v.push_back({"magnitude", t.offM, cols ? t.in : t.out});
   }
+  return v;
+}
+
+static int write_adapter_file(DitModel& m, const std::string& path, std::string& err) {
   std::vector<float> p;
   if (fetch_flat(m, m.p, p, err)) return 1;
   std::vector<AdapterTargetView> v;
+  std::vector<std::vector<float>> bases;   // the -xs U / V of each target, read back
+  bases.reserve(2 * m.tg.size());
   for (size_t i : file_order(m)) {
     const DitTarget& t = m.tg[i];
     AdapterTargetView a;
     a.stem = stem_of(t.name);
     a.in = t.in;
     a.out = t.out;
-    a.A = p.data() + t.offA;
-    a.B = p.data() + t.offB;
-    a.m = t.offM >= 0 ? p.data() + t.offM : nullptr;
+    for (const Part& q : target_parts(m, t)) {
+      const float* d = p.data() + q.off;
+      const std::string k = q.kind;
+      if (k == "lora_A") a.A = d;
+      else if (k == "lora_B") a.B = d;
+      else if (k == "M_xs") a.M = d;
+      else if (k == "magnitude") { a.m = d; a.m_len = q.count; }
+      else if (k == "magnitude_r") a.m_r = d;
+      else a.m_c = d;
+    }
+    if (t.offX >= 0) {
+      if (!t.U) {
+        err = "the -xs target " + t.name + " has no device bases to write";
+        return 1;
+      }
+      bases.emplace_back((size_t)(t.out * m.rank));
+      bases.emplace_back((size_t)(t.in * m.rank));
+      if (cudaMemcpy(bases[bases.size() - 2].data(), t.U, 4 * (size_t)t.out * m.rank, cudaMemcpyDeviceToHost) !=
+              cudaSuccess ||
+          cudaMemcpy(bases.back().data(), t.Vb, 4 * (size_t)t.in * m.rank, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        err = "basis read-back failed";
+        return 1;
+      }
+      a.U = bases[bases.size() - 2].data();
+      a.V = bases.back().data();
+    }
     v.push_back(a);
   }
   return write_adapter_gguf(path, adapter_type_of(m), m.rank, m.alpha, v, err) ? 0 : 1;
@@ -1479,11 +1523,14 @@ static int write_adapter_file(DitModel& m, const std::string& path, std::string&
 // The adapter values of `path` into the host copy `p` of the flat parameters, with the checks of
 // train_restore_adapter_values (src/train_resume.h:104-148): same type, rank and alpha, the same
 // set of targets, every tensor of the expected size.
-static int read_adapter_file(const DitModel& m, const std::string& path, std::vector<float>& p, std::string& err) {
-  if (m.mat) {
-    err = "adapter files are read for lora and dora-rows adapters only (not " + m.adapter_type + ")";
-    return 1;
-  }
+// bases: for -xs adapters, U and V of each target (index into m.tg), uploaded by the caller once
+// the whole file has been checked.
+struct XsBases {
+  size_t target;
+  std::vector<float> U, V;
+};
+static int read_adapter_file(const DitModel& m, const std::string& path, std::vector<float>& p,
+                             std::vector<XsBases>& bases, std::string& err) {
   GgufFile f;
   if (!f.open(path, err)) return 1;
   const GgufValue* ty = f.find("lora.adapter_type");
@@ -1498,18 +1545,21 @@ static int read_adapter_file(const DitModel& m, const std::string& path, std::ve
     err = "adapter type/rank/alpha of " + path + " does not match the model's adapters";
     return 1;
   }
+  const GgufValue* nt = f.find("lora.n_targets");
   size_t stems = 0;
-  for (const std::string& n : f.tensor_order)
-    if (n.size() > 7 && n.compare(n.size() - 7, 7, ".lora_A") == 0) ++stems;
+  if (nt && nt->type == kGgufU32) {
+    stems = (size_t)nt->u;
+  } else {
+    for (const std::string& n : f.tensor_order)
+      if (n.size() > 7 && n.compare(n.size() - 7, 7, ".lora_A") == 0) ++stems;
+  }
   if (stems != m.tg.size()) {
     err = "adapter file target count does not match the model's adapters";
     return 1;
   }
   for (const DitTarget& t : m.tg) {
     const std::string st = stem_of(t.name);
-    struct Part { const char* kind; int64_t off, count; };
-    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
-    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    const std::vector<Part> parts = target_parts(m, t);
     for (const Part& q : parts) {
       std::vector<float> v;
       const std::string name = st + "." + q.kind;
@@ -1523,6 +1573,33 @@ static int read_adapter_file(const DitModel& m, const std::string& path, std::ve
         return 1;
       }
       std::copy(v.begin(), v.end(), p.begin() + q.off);
+    }
+    if (t.offX >= 0) {
+      XsBases b;
+      b.target = (size_t)(&t - m.tg.data());
+      if (!f.tensors.count(st + ".U") || !f.tensors.count(st + ".V")) {
+        err = "adapter file is missing the -xs bases of " + st;
+        return 1;
+      }
+      if (!f.read_f32(st + ".U", b.U, err) || !f.read_f32(st + ".V", b.V, err)) return 1;
+      if ((int64_t)b.U.size() != t.out * m.rank || (int64_t)b.V.size() != t.in * m.rank) {
+        err = "adapter basis shape mismatch: " + st;
+        return 1;
+      }
+      bases.push_back(std::move(b));
+    }
+  }
+  return 0;
+}
+
+static int upload_bases(DitModel& m, const std::vector<XsBases>& bases, std::string& err) {
+  for (const XsBases& b : bases) {
+    const DitTarget& t = m.tg[b.target];
+    if (!t.U) continue;   // an inert target keeps no device bases
+    if (cudaMemcpy(t.U, b.U.data(), 4 * b.U.size(), cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(t.Vb, b.V.data(), 4 * b.V.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+      err = "basis upload failed";
+      return 1;
     }
   }
   return 0;
@@ -1555,7 +1632,9 @@ int sa3k_dit_load_adapter(sa3k_dit* d, const char* path, char* err, int err_len)
   cudaSetDevice(m.c->device);
   std::string e;
   std::vector<float> p((size_t)m.np, 0.f);
-  if (read_adapter_file(m, path, p, e) || store_flat(m, m.p, p, e)) return dfail(err, err_len, e);
+  std::vector<XsBases> bases;
+  if (read_adapter_file(m, path, p, bases, e) || store_flat(m, m.p, p, e) || upload_bases(m, bases, e))
+    return dfail(err, err_len, e);
   return 0;
 }
 
@@ -1616,9 +1695,7 @@ int sa3k_dit_save_checkpoint(sa3k_dit* d, const char* adapter_path, const char* 
   for (size_t i : file_order(m)) {
     const DitTarget& t = m.tg[i];
     const std::string base = "optimizer." + stem_of(t.name) + ".";
-    struct Part { const char* kind; int64_t off, count; };
-    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
-    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    const std::vector<Part> parts = target_parts(m, t);
     for (const Part& q : parts) {
       w.add_f32(base + q.kind + ".m", {q.count}, mom.data() + q.off);
       w.add_f32(base + q.kind + ".v", {q.count}, vel.data() + q.off);
@@ -1667,12 +1744,11 @@ int sa3k_dit_load_checkpoint(sa3k_dit* d, const char* adapter_path, const char* 
   if (!tg || tg->type != kGgufArray || tg->arr_type != kGgufString || tg->arr_s != stems)
     return dfail(err, err_len, "trainer state target inventory does not match the model's adapters");
   std::vector<float> p((size_t)m.np, 0.f), mom((size_t)m.np, 0.f), vel((size_t)m.np, 0.f);
-  if (read_adapter_file(m, adapter_path, p, e)) return dfail(err, err_len, e);
+  std::vector<XsBases> bases;
+  if (read_adapter_file(m, adapter_path, p, bases, e)) return dfail(err, err_len, e);
   for (const DitTarget& t : m.tg) {
     const std::string base = "optimizer." + stem_of(t.name) + ".";
-    struct Part { const char* kind; int64_t off, count; };
-    std::vector<Part> parts = {{"lora_A", t.offA, (int64_t)m.rank * t.in}, {"lora_B", t.offB, t.out * m.rank}};
-    if (t.offM >= 0) parts.push_back({"magnitude", t.offM, t.out});
+    const std::vector<Part> parts = target_parts(m, t);
     for (const Part& q : parts) {
       for (int k = 0; k < 2; ++k) {
         const std::string name = base + q.kind + (k ? ".v" : ".m");
@@ -1684,7 +1760,8 @@ int sa3k_dit_load_checkpoint(sa3k_dit* d, const char* adapter_path, const char* 
       }
     }
   }
-  if (store_flat(m, m.p, p, e) || store_flat(m, m.am, mom, e) || store_flat(m, m.av, vel, e))
+  if (store_flat(m, m.p, p, e) || store_flat(m, m.am, mom, e) || store_flat(m, m.av, vel, e) ||
+      upload_bases(m, bases, e))
     return dfail(err, err_len, e);
   *step = (int64_t)st->u;
   return 0;

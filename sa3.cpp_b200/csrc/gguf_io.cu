@@ -350,9 +350,14 @@ bool write_adapter_gguf(const std::string& path, const std::string& adapter_type
   w.set_f32("lora.alpha", alpha);
   w.set_u32("lora.n_targets", (uint32_t)targets.size());
   for (const AdapterTargetView& t : targets) {
-    w.add_f32(t.stem + ".lora_A", {t.in, rank}, t.A);
-    w.add_f32(t.stem + ".lora_B", {rank, t.out}, t.B);
-    if (t.m) w.add_f32(t.stem + ".magnitude", {t.out}, t.m);
+    if (t.A) w.add_f32(t.stem + ".lora_A", {t.in, rank}, t.A);
+    if (t.B) w.add_f32(t.stem + ".lora_B", {rank, t.out}, t.B);
+    if (t.U) w.add_f32(t.stem + ".U", {rank, t.out}, t.U);
+    if (t.V) w.add_f32(t.stem + ".V", {rank, t.in}, t.V);
+    if (t.M) w.add_f32(t.stem + ".M_xs", {rank, rank}, t.M);
+    if (t.m) w.add_f32(t.stem + ".magnitude", {t.m_len > 0 ? t.m_len : t.out}, t.m);
+    if (t.m_r) w.add_f32(t.stem + ".magnitude_r", {t.out}, t.m_r);
+    if (t.m_c) w.add_f32(t.stem + ".magnitude_c", {t.in}, t.m_c);
   }
   const std::string tmp = path + ".tmp";
   std::remove(tmp.c_str());

@@ -71,14 +71,22 @@ struct GgufFile {
 };
 
 // One adapter target as the adapter file stores it (write_train_lora_gguf,
-// src/train_checkpoint.h:42-113): <stem>.lora_A F32 ne {in, rank} (= A [rank][in]),
-// <stem>.lora_B ne {rank, out} (= B [out][rank]), <stem>.magnitude ne {out} (dora-rows only).
+// src/train_checkpoint.h:42-113), tensors in this order where present: <stem>.lora_A F32 ne
+// {in, rank} (= A [rank][in]), .lora_B ne {rank, out} (= B [out][rank]), .U ne {rank, out},
+// .V ne {rank, in}, .M_xs ne {rank, rank}, .magnitude, .magnitude_r ne {out}, .magnitude_c
+// ne {in}.
 struct AdapterTargetView {
   std::string stem;
   int64_t in = 0, out = 0;
-  const float* A = nullptr;
+  const float* A = nullptr;     // standard families
   const float* B = nullptr;
-  const float* m = nullptr;   // null: no magnitude tensor
+  const float* U = nullptr;     // -xs: U [out][rank], V [in][rank] (frozen), M_xs [rank][rank]
+  const float* V = nullptr;
+  const float* M = nullptr;
+  const float* m = nullptr;     // magnitude (dora-rows [out], dora-cols [in]); null: none
+  int64_t m_len = 0;            // its length (0: out)
+  const float* m_r = nullptr;   // bora [out]
+  const float* m_c = nullptr;   // bora [in]
 };
 // Writes the adapter file (metadata general.architecture "sa3-lora", general.name, lora.adapter_type,
 // lora.rank, lora.alpha, lora.n_targets; tensors in target order) through path + ".tmp" and a rename.
