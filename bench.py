@@ -422,7 +422,7 @@ def dit_attention_flops(cfg, B, T, C):
     return cfg["depth"] * (self_f * (1 + 2.5) + cross_f * (1 + 1.5))
 
 
-def build_dit(ctx, cfg, seed):
+def build_dit(ctx, cfg, seed, adapter_type="dora-rows"):
     """A seeded synthetic checkpoint uploaded as GGUF Q8_0 rows (weights made and encoded on the GPU)."""
     import torch
     import sa3k
@@ -440,16 +440,22 @@ def build_dit(ctx, cfg, seed):
             v = dit_synth.synth_tensor(name, shape, rng, 0.0)
             dit.set_tensor(name, "f32", v, shape[-1], shape[0] if len(shape) > 1 else 1)
     targets = dit_synth.default_targets(cfg)
-    dit.init_adapters("dora-rows", DIT_RANK, DIT_ALPHA, targets)
-    # A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.01) so every gradient is non-trivial; m = base row norms
+    dit.init_adapters(adapter_type, DIT_RANK, DIT_ALPHA, targets)
+    # A ~ N(0, 1/sqrt(in)), B ~ N(0, 0.01) so every gradient is non-trivial; magnitudes = base
+    # row / column norms; -xs: orthonormal random bases and M ~ N(0, 0.1)
     shapes = dit_synth.tensor_shapes(cfg)
     p = torch.empty(dit.size(), device="cuda")
     dit.copy(0, p, to_model=False)
     for i, name in enumerate(targets):
-        oa, ob, _ = dit.offsets(i)
+        oa, ob, _, _, ox = dit.layout(i)
         out, inn = shapes[name]
-        p[oa:oa + DIT_RANK * inn].normal_(0.0, 1.0 / np.sqrt(inn), generator=gen)
-        p[ob:ob + out * DIT_RANK].normal_(0.0, 0.01, generator=gen)
+        if oa >= 0:
+            p[oa:oa + DIT_RANK * inn].normal_(0.0, 1.0 / np.sqrt(inn), generator=gen)
+            p[ob:ob + out * DIT_RANK].normal_(0.0, 0.01, generator=gen)
+        if ox >= 0:
+            p[ox:ox + DIT_RANK * DIT_RANK].normal_(0.0, 0.1, generator=gen)
+            dit.set_xs_bases(name, np.linalg.qr(rng.standard_normal((out, DIT_RANK)))[0],
+                             np.linalg.qr(rng.standard_normal((inn, DIT_RANK)))[0])
     dit.copy(0, p, to_model=True)
     torch.cuda.synchronize()
     return dit
@@ -587,7 +593,7 @@ def main_dit(args):
         cfg["depth"] = args.depth   # profiling of per-block kernels on a shallower stack only
     B, T, C = DIT_B, DIT_T, DIT_CTX
     ctx = sa3k.Context(local)
-    dit = build_dit(ctx, cfg, seed=1234)                 # identical base + adapters on every rank
+    dit = build_dit(ctx, cfg, seed=1234, adapter_type=args.adapter_type)   # identical on every rank
     comm = None
     if world > 1:   # the library's own NCCL clique for the gradient all-reduce (sa3k_dp_*)
         import dp
@@ -721,7 +727,8 @@ def main_dit(args):
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": DIT_WORKLOAD + (f" (depth overridden to {cfg['depth']})" if args.depth else ""),
+            "config": {"workload": DIT_WORKLOAD + (f" (depth overridden to {cfg['depth']})" if args.depth else "")
+                       + (f" (adapters overridden to {args.adapter_type})" if args.adapter_type != "dora-rows" else ""),
                        "global_batch": B * world, "seq_len": T,
                        "parallelism": f"dp{world}", "l2": "256 MB flush between timed steps"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
@@ -854,6 +861,9 @@ def main():
     ap.add_argument("--depth", type=int, default=0,
                     help="dit: override the block count (small device footprint for ncu captures of per-block "
                          "kernels; the benchmark line is quoted at the configured 24)")
+    ap.add_argument("--adapter-type", default="dora-rows",
+                    help="dit: adapter family of the step (the benchmark line is quoted with dora-rows; the "
+                         "materialized families time their per-step W_eff build and weight-gradient passes)")
     ap.add_argument("--profile-step", action="store_true",
                     help="dit: bracket one extra graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     args = ap.parse_args()

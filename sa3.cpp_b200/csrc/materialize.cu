@@ -31,7 +31,6 @@ namespace sa3k {
 namespace {
 
 constexpr float kMatEps = 1e-12f;
-constexpr int kMatRows = 8;        // rows per block of the row kernels (one warp per row)
 constexpr int kMatMaxRank = 16;
 constexpr int kSlotMat = 57;
 
@@ -65,41 +64,63 @@ __global__ void mat_xs_prep_kernel(const float* __restrict__ U, const float* __r
   }
 }
 
-// V = W + s P Q, one warp per row; rn2[o] = sum_i V^2 + in eps (f64 sum) and rs[o] = mr[o] /
-// sqrt(rn2[o]) (1 without a row magnitude).  Q rows are read through L1 by the block's 8 rows.
-__global__ void __launch_bounds__(256) mat_build_kernel(const Weight w, const float* __restrict__ P,
-                                                        const float* __restrict__ Q, int r, float s,
-                                                        const float* __restrict__ mr, float* __restrict__ V,
-                                                        double* __restrict__ rn2, float* __restrict__ rs) {
-  __shared__ float ps[kMatRows][kMatMaxRank];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t o = (int64_t)blockIdx.x * kMatRows + warp;
-  if (o >= w.out) return;
-  if (lane < r) ps[warp][lane] = s * P[o * r + lane];
-  __syncwarp();
-  const int64_t in = w.in;
-  double acc = 0.0;
-  for (int64_t i = 4 * lane; i < in; i += 128) {
-    float v[4];
+// V = W + s P Q; rn2[o] = sum_i V^2 + in eps (f64 sum) and rs[o] = mr[o] / sqrt(rn2[o]) (1
+// without a row magnitude).  A block of 128 threads takes two rows, its threads spread over the
+// columns; each Q chunk read serves both rows, and the row sums are reduced in shared memory.
+constexpr int kBdThreads = 128, kBdRows = 2, kBdWarps = kBdThreads / 32;
+__global__ void __launch_bounds__(kBdThreads) mat_build_kernel(const Weight w, const float* __restrict__ P,
+                                                               const float* __restrict__ Q, int r, float s,
+                                                               const float* __restrict__ mr, float* __restrict__ V,
+                                                               double* __restrict__ rn2, float* __restrict__ rs) {
+  __shared__ float ps[kBdRows][kMatMaxRank];
+  __shared__ double red[kBdWarps][kBdRows];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t o0 = (int64_t)blockIdx.x * kBdRows, in = w.in;
+  const int nr = (int)min((int64_t)kBdRows, w.out - o0);
+  if (tid < kBdRows * kMatMaxRank) {
+    const int u = tid / kMatMaxRank, j = tid % kMatMaxRank;
+    ps[u][j] = (u < nr && j < r) ? s * P[(o0 + u) * r + j] : 0.f;
+  }
+  __syncthreads();
+  double acc[kBdRows] = {0.0, 0.0};
+  for (int64_t i = 4 * tid; i < in; i += 4 * kBdThreads) {
+    float v[kBdRows][4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) v[c] = wval(w, o, i + c);
+    for (int u = 0; u < kBdRows; ++u) {
+      if (u < nr) wval4(w, o0 + u, i, v[u]);
+      else v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+    }
     for (int j = 0; j < r; ++j) {
       const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
-      const float pj = ps[warp][j];
-      v[0] = fmaf(pj, q.x, v[0]);
-      v[1] = fmaf(pj, q.y, v[1]);
-      v[2] = fmaf(pj, q.z, v[2]);
-      v[3] = fmaf(pj, q.w, v[3]);
-    }
-    *reinterpret_cast<float4*>(V + o * in + i) = make_float4(v[0], v[1], v[2], v[3]);
 #pragma unroll
-    for (int c = 0; c < 4; ++c) acc += (double)v[c] * (double)v[c];
+      for (int u = 0; u < kBdRows; ++u) {
+        const float pj = ps[u][j];
+        v[u][0] = fmaf(pj, q.x, v[u][0]);
+        v[u][1] = fmaf(pj, q.y, v[u][1]);
+        v[u][2] = fmaf(pj, q.z, v[u][2]);
+        v[u][3] = fmaf(pj, q.w, v[u][3]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBdRows; ++u) {
+      if (u >= nr) break;
+      *reinterpret_cast<float4*>(V + (o0 + u) * in + i) = make_float4(v[u][0], v[u][1], v[u][2], v[u][3]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[u] += (double)v[u][c] * (double)v[u][c];
+    }
   }
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const double n2 = acc + (double)in * (double)kMatEps;
-    rn2[o] = n2;
-    rs[o] = mr ? mr[o] / (float)sqrt(n2) : 1.0f;
+#pragma unroll
+  for (int u = 0; u < kBdRows; ++u) {
+    const double t = warp_sum(acc[u]);
+    if (lane == 0) red[warp][u] = t;
+  }
+  __syncthreads();
+  if (tid < nr) {
+    double n2 = (double)in * (double)kMatEps;
+#pragma unroll
+    for (int k = 0; k < kBdWarps; ++k) n2 += red[k][tid];
+    rn2[o0 + tid] = n2;
+    rs[o0 + tid] = mr ? mr[o0 + tid] / (float)sqrt(n2) : 1.0f;
   }
 }
 
@@ -517,8 +538,8 @@ int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPla
   }
   {
     ProfScope prof_(c, "mat.build");
-    mat_build_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(*w, P, Q, r, ad->scale, p.mr, b.V,
-                                                                                  b.rn2, b.rs);
+    mat_build_kernel<<<(unsigned)((out + kBdRows - 1) / kBdRows), kBdThreads, 0, st>>>(*w, P, Q, r, ad->scale, p.mr,
+                                                                                      b.V, b.rn2, b.rs);
     if (check_launch("mat build", err)) return 1;
   }
   if (p.cols) {
@@ -685,9 +706,9 @@ int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
   }
   {
     ProfScope prof_(c, "mat.build");
-    mat_build_kernel<<<(unsigned)((out + kMatRows - 1) / kMatRows), 256, 0, st>>>(*t.w, P, Q, r, t.s,
-                                                                                  t.rows ? t.mr : nullptr, t.V,
-                                                                                  t.rn2, t.rs);
+    mat_build_kernel<<<(unsigned)((out + kBdRows - 1) / kBdRows), kBdThreads, 0, st>>>(*t.w, P, Q, r, t.s,
+                                                                                      t.rows ? t.mr : nullptr, t.V,
+                                                                                      t.rn2, t.rs);
     if (check_launch("mat build", err)) return 1;
   }
   if (t.cols) {
