@@ -396,19 +396,35 @@ __global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __res
   }
 }
 
-// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld], 32 x 32 tiles.
+// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld] (out and ld even), 64 x 64 tiles:
+// every thread moves bf16 pairs, so a warp reads and writes 128 contiguous bytes.
 __global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t S, int64_t out,
                                            __nv_bfloat16* __restrict__ dst, int64_t ld) {
-  __shared__ __nv_bfloat16 t[32][34];
-  const int64_t s0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t s = s0 + k, o = o0 + threadIdx.x;
-    t[k][threadIdx.x] = (s < S && o < out) ? src[s * out + o] : __float2bfloat16_rn(0.f);
+  __shared__ __nv_bfloat16 t[64][66];   // [s][o], padded
+  const int64_t s0 = (int64_t)blockIdx.x * 64, o0 = (int64_t)blockIdx.y * 64;
+  const int tx = threadIdx.x;
+  const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+  for (int k = threadIdx.y; k < 64; k += blockDim.y) {
+    const int64_t s = s0 + k, o = o0 + 2 * tx;
+    __nv_bfloat162 v;
+    v.x = zero;
+    v.y = zero;
+    if (s < S && o < out) v = *reinterpret_cast<const __nv_bfloat162*>(src + s * out + o);   // out even
+    t[k][2 * tx] = v.x;
+    t[k][2 * tx + 1] = v.y;
   }
   __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t o = o0 + k, s = s0 + threadIdx.x;
-    if (o < out && s < S) dst[o * ld + s] = t[threadIdx.x][k];
+  for (int k = threadIdx.y; k < 64; k += blockDim.y) {
+    const int64_t o = o0 + k, s = s0 + 2 * tx;
+    if (o >= out || s >= S) continue;
+    if (s + 1 < S) {
+      __nv_bfloat162 v;
+      v.x = t[2 * tx][k];
+      v.y = t[2 * tx + 1][k];
+      *reinterpret_cast<__nv_bfloat162*>(dst + o * ld + s) = v;   // ld and s even
+    } else {
+      dst[o * ld + s] = t[2 * tx][k];
+    }
   }
 }
 
@@ -732,13 +748,13 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   const int64_t in = t.in, out = t.out;
   const int r = t.rank;
   const cudaStream_t st = c->stream;
-  if (ldt < M || ldt % 8) {
-    err = "mat backward: transposed gradient pitch";
+  if (ldt < M || ldt % 8 || out % 2) {
+    err = "mat backward: transposed gradient pitch (or an odd output width)";
     return 1;
   }
   {
     ProfScope prof_(c, "mat.transpose");
-    transpose_bf16_bf16_kernel<<<dim3((unsigned)((M + 31) / 32), (unsigned)((out + 31) / 32)), dim3(32, 8), 0, st>>>(
+    transpose_bf16_bf16_kernel<<<dim3((unsigned)((M + 63) / 64), (unsigned)((out + 63) / 64)), dim3(32, 8), 0, st>>>(
         dz, M, out, dzt, ldt);
     if (check_launch("mat transpose", err)) return 1;
   }
