@@ -105,6 +105,7 @@ struct DitModel {
   std::string adapter_type = "lora";
   float* mat_G = nullptr;              // [max out*in] f32 weight-gradient scratch (materialized)
   __nv_bfloat16* mat_dzt = nullptr;    // [max out][mat_ldt] bf16 transposed output gradient
+  __nv_bfloat16* mat_dD = nullptr;     // [max out*in] bf16 dD of the normalisation backward
   int64_t mat_ldt = 0;
   int rank = 0;
   float alpha = 1.f, s = 1.f;
@@ -418,6 +419,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       }
       m.mat_ldt = (mr + 7) / 8 * 8;
       m.mat_G = f(wn);
+      m.mat_dD = h(wn);
       m.mat_dzt = h(mo * m.mat_ldt);
     }
     if (pass == 0) {
@@ -475,7 +477,7 @@ static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias
       g.name = "linear.dx";
       if (gemm(m.c, g, err)) return 1;
     }
-    return mat_target_backward(m.c, t->mt, m.dz, M, x, m.mat_G, m.mat_dzt, m.mat_ldt, err);
+    return mat_target_backward(m.c, t->mt, m.dz, M, x, m.mat_G, m.mat_dzt, m.mat_ldt, m.mat_dD, err);
   }
   LinearBwd b;
   b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;

@@ -226,7 +226,10 @@ __global__ void transpose_bf16_kernel(const float* __restrict__ src, int64_t S, 
 // A block of 128 threads takes two rows, its threads spread over the columns (many warps per SM
 // even for 1536-row weights); each Q chunk read serves both rows, and the row sums are reduced
 // through shared memory.
+// kBf16Out: dD goes to dDb as bf16 (the operand of the dB / dA GEMMs) instead of back into G,
+// and the rank-r products are left to those GEMMs.
 constexpr int kRbThreads = 128, kRbRows = 2, kRbWarps = kRbThreads / 32;
+template <bool kBf16Out>
 __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restrict__ G, const float* __restrict__ V,
                                                                 const float* __restrict__ rs,
                                                                 const double* __restrict__ rn2,
@@ -235,7 +238,8 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
                                                                 const float* __restrict__ Q, int64_t out, int64_t in,
                                                                 int r, float s, int rows, int cols,
                                                                 float* __restrict__ dmr, float* __restrict__ PG,
-                                                                int acc_pg, int acc_dm) {
+                                                                int acc_pg, int acc_dm,
+                                                                __nv_bfloat16* __restrict__ dDb) {
   __shared__ double red_t[kRbWarps][kRbRows];
   __shared__ float red_a[kRbWarps][kRbRows * kMatMaxRank];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -312,33 +316,44 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
       const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
       for (int c = 0; c < 4; ++c) d[u][c] = s * (rows ? ro[u] * (d[u][c] - vx[c] * t_over[u]) : d[u][c]);
-      *reinterpret_cast<float4*>(g) = make_float4(d[u][0], d[u][1], d[u][2], d[u][3]);
+      if (kBf16Out) {
+        uint2 pk;
+        pk.x = pack_bf16x2(d[u][0], d[u][1]);
+        pk.y = pack_bf16x2(d[u][2], d[u][3]);
+        *reinterpret_cast<uint2*>(dDb + (o0 + u) * in + i) = pk;
+      } else {
+        *reinterpret_cast<float4*>(g) = make_float4(d[u][0], d[u][1], d[u][2], d[u][3]);
+      }
     }
+    if constexpr (!kBf16Out) {
 #pragma unroll
-    for (int j = 0; j < kMatMaxRank; ++j) {
-      if (j >= r) break;
-      const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
+      for (int j = 0; j < kMatMaxRank; ++j) {
+        if (j >= r) break;
+        const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
 #pragma unroll
-      for (int u = 0; u < kRbRows; ++u)
-        acc[u][j] = fmaf(d[u][0], q.x, fmaf(d[u][1], q.y, fmaf(d[u][2], q.z, fmaf(d[u][3], q.w, acc[u][j]))));
+        for (int u = 0; u < kRbRows; ++u)
+          acc[u][j] = fmaf(d[u][0], q.x, fmaf(d[u][1], q.y, fmaf(d[u][2], q.z, fmaf(d[u][3], q.w, acc[u][j]))));
+      }
     }
   }
+  if constexpr (!kBf16Out) {
 #pragma unroll
-  for (int u = 0; u < kRbRows; ++u)
+    for (int u = 0; u < kRbRows; ++u)
 #pragma unroll
-    for (int j = 0; j < kMatMaxRank; ++j) {
-      if (j >= r) break;
-      const float a = warp_sumf(acc[u][j]);
-      if (lane == 0) red_a[warp][u * kMatMaxRank + j] = a;
-    }
-  __syncthreads();
-  if (tid < kRbRows * kMatMaxRank) {
-    const int u = tid / kMatMaxRank, j = tid % kMatMaxRank;
-    if (u < nr && j < r) {
-      float a = 0.f;
+      for (int j = 0; j < kMatMaxRank; ++j) {
+        if (j >= r) break;
+        const float a = warp_sumf(acc[u][j]);
+        if (lane == 0) red_a[warp][u * kMatMaxRank + j] = a;
+      }
+    __syncthreads();
+    if (tid < kRbRows * kMatMaxRank) {
+      const int u = tid / kMatMaxRank, j = tid % kMatMaxRank;
+      if (u < nr && j < r) {
+        float a = 0.f;
 #pragma unroll
-      for (int k = 0; k < kRbWarps; ++k) a += red_a[k][tid];
-      PG[(o0 + u) * r + j] = a + (acc_pg ? PG[(o0 + u) * r + j] : 0.f);
+        for (int k = 0; k < kRbWarps; ++k) a += red_a[k][tid];
+        PG[(o0 + u) * r + j] = a + (acc_pg ? PG[(o0 + u) * r + j] : 0.f);
+      }
     }
   }
 }
@@ -438,6 +453,21 @@ __global__ void mat_col_norms_kernel(const Weight w, float* __restrict__ nrm) {
     a += v * v;
   }
   nrm[i] = (float)sqrt(a);
+}
+
+// Per-step bf16 operands of the weight-gradient GEMMs: Qb [r][in] = Q (A, or V^T for -xs) and,
+// for the standard families, Btb [r][out] = B^T.
+__global__ void mat_pack_kernel(const float* __restrict__ Q, const float* __restrict__ B, int64_t out, int64_t in,
+                                int r, __nv_bfloat16* __restrict__ Qb, __nv_bfloat16* __restrict__ Btb) {
+  const int64_t n1 = (int64_t)r * in, n = n1 + (B ? (int64_t)r * out : 0);
+  for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
+    if (k < n1) {
+      Qb[k] = __float2bfloat16_rn(Q[k]);
+    } else {
+      const int64_t q = k - n1, j = q / out, o = q % out;
+      Btb[q] = __float2bfloat16_rn(B[o * r + j]);
+    }
+  }
 }
 
 struct MatPlan {
@@ -650,9 +680,9 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   }
   {
     ProfScope prof_(c, "mat.rows_bwd");
-    mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
+    mat_rowbwd_kernel<false><<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
         b.G, b.V, b.rs, b.rn2, b.cs, b.tcn, Q, out, in, r, ad->scale, p.rows ? 1 : 0, p.cols ? 1 : 0,
-        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB, 0, 0);
+        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB, 0, 0, nullptr);
     if (check_launch("mat rows bwd", err)) return 1;
   }
   if (p.xs) {
@@ -682,7 +712,7 @@ size_t mat_target_bytes(int64_t in, int64_t out, int rank) {
   auto al = [](size_t b) { return (b + 255) / 256 * 256; };
   const size_t wn = (size_t)(in * out);
   return al(4 * wn) + al(2 * wn) + 2 * al(4 * (size_t)out * rank) + al(4 * (size_t)rank * in) + al(4 * out) +
-         2 * al(4 * in) + al(8 * out) + 2 * al(8 * in);
+         2 * al(4 * in) + al(8 * out) + 2 * al(8 * in) + al(2 * (size_t)rank * in) + al(2 * (size_t)rank * out);
 }
 
 void mat_target_bind(MatTarget& t, void* mem) {
@@ -701,6 +731,8 @@ void mat_target_bind(MatTarget& t, void* mem) {
   t.rn2 = reinterpret_cast<double*>(take(8 * t.out));
   t.csq = reinterpret_cast<double*>(take(8 * t.in));
   t.tc = reinterpret_cast<double*>(take(8 * t.in));
+  t.Qb = reinterpret_cast<__nv_bfloat16*>(take(2 * (size_t)t.rank * t.in));
+  t.Btb = reinterpret_cast<__nv_bfloat16*>(take(2 * (size_t)t.rank * t.out));
 }
 
 int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
@@ -740,11 +772,13 @@ int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
                                                                  t.cs, nullptr, nullptr, 0);
   if (check_launch("mat colfac", err)) return 1;
   mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(t.V, t.rs, t.cs, out, in, t.wb, nullptr);
-  return check_launch("mat weff", err);
+  if (check_launch("mat weff", err)) return 1;
+  mat_pack_kernel<<<(unsigned)(c->sm_count), 256, 0, st>>>(Q, t.xs ? nullptr : t.B, out, in, r, t.Qb, t.Btb);
+  return check_launch("mat pack", err);
 }
 
 int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M, const __nv_bfloat16* x,
-                        float* G, __nv_bfloat16* dzt, int64_t ldt, std::string& err) {
+                        float* G, __nv_bfloat16* dzt, int64_t ldt, __nv_bfloat16* dDb, std::string& err) {
   const int64_t in = t.in, out = t.out;
   const int r = t.rank;
   const cudaStream_t st = c->stream;
@@ -779,21 +813,36 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   }
   {
     ProfScope prof_(c, "mat.rows_bwd");
-    mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
-        G, t.V, t.rs, t.rn2, t.cs, t.tcn, t.xs ? t.Q : t.A, out, in, r, t.s, t.rows ? 1 : 0, t.cols ? 1 : 0,
-        t.rows ? t.dmr : nullptr, t.xs ? t.PG : t.dB, t.xs ? 0 : 1, 1);
+    mat_rowbwd_kernel<true><<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
+        G, t.V, t.rs, t.rn2, t.cs, t.tcn, nullptr, out, in, r, t.s, t.rows ? 1 : 0, t.cols ? 1 : 0,
+        t.rows ? t.dmr : nullptr, nullptr, 0, 1, dDb);
     if (check_launch("mat rows bwd", err)) return 1;
+  }
+  if (t.xs && cudaMemsetAsync(t.PG, 0, sizeof(float) * (size_t)out * r, st) != cudaSuccess)
+    return check_launch("memset", err);
+  {
+    GemmDesc d;   // dB += dD A^T, or PG = dD V (-xs)  [out][r], K = in
+    d.M = (int)out; d.N = r; d.K = (int)in;
+    d.a = dDb; d.lda = in;
+    d.bsrc = kB_BF16_KMAJOR; d.b = t.Qb; d.ldb = in;
+    d.out = t.xs ? t.PG : t.dB; d.ldo = r; d.accumulate = 1; d.bn = 16;
+    d.atomic_split = 1;
+    d.name = "mat.dB";
+    if (gemm(c, d, err)) return 1;
   }
   if (t.xs) {
     ProfScope prof_(c, "mat.dM");
     mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(t.U, t.PG, out, r, t.dM, 1);
     return check_launch("mat dM", err);
   }
-  ProfScope prof_(c, "mat.dA");
-  const int64_t rp = col_rows_per(c, out, in, 256);
-  mat_da_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
-      G, t.B, out, in, r, rp, t.dA);
-  return check_launch("mat dA", err);
+  GemmDesc d;   // dA^T += dD^T B  [in][r] (dD read MN-major), stored transposed as dA [r][in]
+  d.M = (int)in; d.N = r; d.K = (int)out;
+  d.a = dDb; d.lda = in; d.a_mn = 1;
+  d.bsrc = kB_BF16_KMAJOR; d.b = t.Btb; d.ldb = out;
+  d.out = t.dA; d.ldo = in; d.out_trans = 1; d.accumulate = 1; d.bn = 16;
+  d.atomic_split = 1;
+  d.name = "mat.dA";
+  return gemm(c, d, err);
 }
 
 int mat_col_norms(Ctx* c, const Weight* w, float* nrm, std::string& err) {

@@ -27,6 +27,7 @@ struct MatTarget {
   float *V = nullptr, *rs = nullptr, *cs = nullptr, *tcn = nullptr, *P = nullptr, *Q = nullptr, *PG = nullptr;
   double *rn2 = nullptr, *csq = nullptr, *tc = nullptr;
   __nv_bfloat16* wb = nullptr;
+  __nv_bfloat16 *Qb = nullptr, *Btb = nullptr;   // bf16 A (or V^T) [rank][in] and B^T [rank][out]
 };
 
 size_t mat_target_bytes(int64_t in, int64_t out, int rank);
@@ -35,9 +36,10 @@ void mat_target_bind(MatTarget& t, void* mem);
 int mat_target_build(Ctx* c, MatTarget& t, std::string& err);
 // The weight gradient of one backward: G = dz^T x (dz [M][out] bf16, x [M][in] bf16, K = M) into
 // G [out][in] f32 scratch (dzt: [out][ldt] bf16 scratch, ldt >= M, a multiple of 8), then the
-// normalisation backward; the adapter gradients are added into t.dA / dB / dM / dmr / dmc.
+// normalisation backward into dD = s dV (dDb: [out][in] bf16 scratch) and the rank-r GEMMs on dD;
+// the adapter gradients are added into t.dA / dB / dM / dmr / dmc.
 int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M, const __nv_bfloat16* x,
-                        float* G, __nv_bfloat16* dzt, int64_t ldt, std::string& err);
+                        float* G, __nv_bfloat16* dzt, int64_t ldt, __nv_bfloat16* dDb, std::string& err);
 // nrm[i] = sqrt(sum_o W[o][i]^2) (f64 sums), the column-magnitude init (train_col_norms,
 // src/train_lora.h:176-190).
 int mat_col_norms(Ctx* c, const Weight* w, float* nrm, std::string& err);
