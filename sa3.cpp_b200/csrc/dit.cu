@@ -600,7 +600,7 @@ static int dit_step(DitModel& m, std::string& err) {
   }
   // materialized families: W_eff of every target from this step's parameters
   for (DitTarget& t : m.tg)
-    if (t.mat && !t.inert && mat_target_build(c, t.mt, err)) return 1;
+    if (t.mat && !t.inert && mat_target_build(c, t.mt, nullptr, err)) return 1;
 
   // ---------------- head (src/dit.h:286-310)
   if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;

@@ -203,45 +203,22 @@ __global__ void mat_weff_kernel(const float* __restrict__ V, const float* __rest
   }
 }
 
-// dst[o][s] = bf16(src[s][o]) (src [S][out] f32 -> dst [out][ld] bf16), 32 x 32 tiles.
-__global__ void transpose_bf16_kernel(const float* __restrict__ src, int64_t S, int64_t out,
-                                      __nv_bfloat16* __restrict__ dst, int64_t ld) {
-  __shared__ float t[32][33];
-  const int64_t s0 = (int64_t)blockIdx.x * 32, o0 = (int64_t)blockIdx.y * 32;
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t s = s0 + k, o = o0 + threadIdx.x;
-    t[k][threadIdx.x] = (s < S && o < out) ? src[s * out + o] : 0.f;
-  }
-  __syncthreads();
-  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
-    const int64_t o = o0 + k, s = s0 + threadIdx.x;
-    if (o < out && s < S) dst[o * ld + s] = __float2bfloat16_rn(t[threadIdx.x][k]);
-  }
-}
-
-// The row pass of the backward, G [out][in] replaced by dD = s dV:
+// The row pass of the backward: dD = s dV as bf16 (the operand of the dB / dA GEMMs):
 //   dR = cols ? cs[i] (G - rs V tcn[i]) : G
-//   rows: t = sum_i dR V, dmr[o] = t / rn, dV = rs (dR - V t / rn^2), else dV = dR
-//   PG[o][j] = sum_i dD Q[j][i] (dB for the standard families, (dD V)[o][j] for -xs).
+//   rows: t = sum_i dR V, dmr[o] += t / rn, dV = rs (dR - V t / rn^2), else dV = dR
 // A block of 128 threads takes two rows, its threads spread over the columns (many warps per SM
-// even for 1536-row weights); each Q chunk read serves both rows, and the row sums are reduced
-// through shared memory.
-// kBf16Out: dD goes to dDb as bf16 (the operand of the dB / dA GEMMs) instead of back into G,
-// and the rank-r products are left to those GEMMs.
+// even for 1536-row weights), and the row sums are reduced through shared memory.
 constexpr int kRbThreads = 128, kRbRows = 2, kRbWarps = kRbThreads / 32;
-template <bool kBf16Out>
-__global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restrict__ G, const float* __restrict__ V,
+__global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(const float* __restrict__ G,
+                                                                const float* __restrict__ V,
                                                                 const float* __restrict__ rs,
                                                                 const double* __restrict__ rn2,
                                                                 const float* __restrict__ cs,
-                                                                const float* __restrict__ tcn,
-                                                                const float* __restrict__ Q, int64_t out, int64_t in,
-                                                                int r, float s, int rows, int cols,
-                                                                float* __restrict__ dmr, float* __restrict__ PG,
-                                                                int acc_pg, int acc_dm,
+                                                                const float* __restrict__ tcn, int64_t out,
+                                                                int64_t in, float s, int rows, int cols,
+                                                                float* __restrict__ dmr,
                                                                 __nv_bfloat16* __restrict__ dDb) {
   __shared__ double red_t[kRbWarps][kRbRows];
-  __shared__ float red_a[kRbWarps][kRbRows * kMatMaxRank];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t o0 = (int64_t)blockIdx.x * kRbRows;
   const int nr = (int)min((int64_t)kRbRows, out - o0);
@@ -291,105 +268,26 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(float* __restric
 #pragma unroll
       for (int k = 0; k < kRbWarps; ++k) tt += red_t[k][u];
       t_over[u] = (float)(tt / rn2[o0 + u]);
-      if (tid == 0) dmr[o0 + u] = (float)(tt / sqrt(rn2[o0 + u])) + (acc_dm ? dmr[o0 + u] : 0.f);
+      if (tid == 0) dmr[o0 + u] += (float)(tt / sqrt(rn2[o0 + u]));
     }
   }
-  float acc[kRbRows][kMatMaxRank];
-#pragma unroll
-  for (int u = 0; u < kRbRows; ++u)
-#pragma unroll
-    for (int j = 0; j < kMatMaxRank; ++j) acc[u][j] = 0.f;
   for (int64_t i = 4 * tid; i < in; i += 4 * kRbThreads) {
     const float4 cf = cols ? *reinterpret_cast<const float4*>(cs + i) : one4;
     const float4 tc = cols ? *reinterpret_cast<const float4*>(tcn + i) : one4;
-    float d[kRbRows][4];
 #pragma unroll
     for (int u = 0; u < kRbRows; ++u) {
-      if (u >= nr) {
-        d[u][0] = d[u][1] = d[u][2] = d[u][3] = 0.f;
-        continue;
-      }
-      float* g = G + (o0 + u) * in + i;
-      const float4 gv = *reinterpret_cast<const float4*>(g);
+      if (u >= nr) break;
+      const float4 gv = *reinterpret_cast<const float4*>(G + (o0 + u) * in + i);
       const float4 vv = *reinterpret_cast<const float4*>(V + (o0 + u) * in + i);
-      dr4(gv, vv, cf, tc, ro[u], d[u]);
+      float d[4];
+      dr4(gv, vv, cf, tc, ro[u], d);
       const float vx[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) d[u][c] = s * (rows ? ro[u] * (d[u][c] - vx[c] * t_over[u]) : d[u][c]);
-      if (kBf16Out) {
-        uint2 pk;
-        pk.x = pack_bf16x2(d[u][0], d[u][1]);
-        pk.y = pack_bf16x2(d[u][2], d[u][3]);
-        *reinterpret_cast<uint2*>(dDb + (o0 + u) * in + i) = pk;
-      } else {
-        *reinterpret_cast<float4*>(g) = make_float4(d[u][0], d[u][1], d[u][2], d[u][3]);
-      }
-    }
-    if constexpr (!kBf16Out) {
-#pragma unroll
-      for (int j = 0; j < kMatMaxRank; ++j) {
-        if (j >= r) break;
-        const float4 q = __ldg(reinterpret_cast<const float4*>(Q + (int64_t)j * in + i));
-#pragma unroll
-        for (int u = 0; u < kRbRows; ++u)
-          acc[u][j] = fmaf(d[u][0], q.x, fmaf(d[u][1], q.y, fmaf(d[u][2], q.z, fmaf(d[u][3], q.w, acc[u][j]))));
-      }
-    }
-  }
-  if constexpr (!kBf16Out) {
-#pragma unroll
-    for (int u = 0; u < kRbRows; ++u)
-#pragma unroll
-      for (int j = 0; j < kMatMaxRank; ++j) {
-        if (j >= r) break;
-        const float a = warp_sumf(acc[u][j]);
-        if (lane == 0) red_a[warp][u * kMatMaxRank + j] = a;
-      }
-    __syncthreads();
-    if (tid < kRbRows * kMatMaxRank) {
-      const int u = tid / kMatMaxRank, j = tid % kMatMaxRank;
-      if (u < nr && j < r) {
-        float a = 0.f;
-#pragma unroll
-        for (int k = 0; k < kRbWarps; ++k) a += red_a[k][tid];
-        PG[(o0 + u) * r + j] = a + (acc_pg ? PG[(o0 + u) * r + j] : 0.f);
-      }
-    }
-  }
-}
-
-// dA[j][i] += sum_{o in slice} B[o][j] dD[o][i] (f32 atomics; dA zeroed first).
-__global__ void __launch_bounds__(256) mat_da_kernel(const float* __restrict__ dD, const float* __restrict__ B,
-                                                     int64_t out, int64_t in, int r, int64_t rows_per,
-                                                     float* __restrict__ dA) {
-  __shared__ float bs[64][kMatMaxRank];
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  const int64_t o0 = (int64_t)blockIdx.y * rows_per, o1 = min(out, o0 + rows_per);
-  float acc[kMatMaxRank];
-#pragma unroll
-  for (int j = 0; j < kMatMaxRank; ++j) acc[j] = 0.f;
-  for (int64_t ob = o0; ob < o1; ob += 64) {
-    const int nb = (int)min((int64_t)64, o1 - ob);
-    __syncthreads();
-    for (int k = threadIdx.x; k < nb * r; k += blockDim.x) bs[k / r][k % r] = B[(ob + k / r) * r + k % r];
-    __syncthreads();
-    if (i < in) {
-#pragma unroll 4
-      for (int q = 0; q < nb; ++q) {
-        const float d = dD[(ob + q) * in + i];
-#pragma unroll
-        for (int j = 0; j < kMatMaxRank; ++j) {
-          if (j >= r) break;
-          acc[j] = fmaf(bs[q][j], d, acc[j]);
-        }
-      }
-    }
-  }
-  if (i < in && o1 > o0) {
-#pragma unroll
-    for (int j = 0; j < kMatMaxRank; ++j) {
-      if (j >= r) break;
-      atomicAdd(dA + (int64_t)j * in + i, acc[j]);
+      for (int c = 0; c < 4; ++c) d[c] = s * (rows ? ro[u] * (d[c] - vx[c] * t_over[u]) : d[c]);
+      uint2 pk;
+      pk.x = pack_bf16x2(d[0], d[1]);
+      pk.y = pack_bf16x2(d[2], d[3]);
+      *reinterpret_cast<uint2*>(dDb + (o0 + u) * in + i) = pk;
     }
   }
 }
@@ -411,8 +309,8 @@ __global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __res
   }
 }
 
-// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld] (out and ld even), 64 x 64 tiles:
-// every thread moves bf16 pairs, so a warp reads and writes 128 contiguous bytes.
+// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld] (ld even), 64 x 64 tiles: every
+// thread moves bf16 pairs, so a warp reads and writes 128 contiguous bytes (even widths).
 __global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t S, int64_t out,
                                            __nv_bfloat16* __restrict__ dst, int64_t ld) {
   __shared__ __nv_bfloat16 t[64][66];   // [s][o], padded
@@ -424,7 +322,14 @@ __global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src
     __nv_bfloat162 v;
     v.x = zero;
     v.y = zero;
-    if (s < S && o < out) v = *reinterpret_cast<const __nv_bfloat162*>(src + s * out + o);   // out even
+    if (s < S && o < out) {
+      if ((out & 1) == 0) {
+        v = *reinterpret_cast<const __nv_bfloat162*>(src + s * out + o);
+      } else {   // odd widths: rows are not 4-byte aligned
+        v.x = src[s * out + o];
+        if (o + 1 < out) v.y = src[s * out + o + 1];
+      }
+    }
     t[k][2 * tx] = v.x;
     t[k][2 * tx + 1] = v.y;
   }
@@ -518,44 +423,6 @@ bool parse_type(const sa3k_mat_adapter* ad, MatPlan& p, std::string& err) {
   return true;
 }
 
-// Device buffers of one call, carved from one scratch slot.
-struct MatBufs {
-  float *V, *G, *P, *Q, *PG, *rs, *cs, *tcn;
-  double *rn2, *csq, *tc;
-  __nv_bfloat16 *wb, *xb, *dyb, *dyt;
-  int64_t ldt;
-};
-
-bool mat_alloc(Ctx* c, int64_t S, int64_t in, int64_t out, int r, bool bwd, MatBufs& b, std::string& err) {
-  const int64_t wn = out * in;
-  b.ldt = (S + 7) / 8 * 8;
-  size_t off = 0;
-  auto take = [&](size_t bytes) { const size_t o = off; off += (bytes + 255) / 256 * 256; return o; };
-  const size_t oV = take(4 * wn), oG = bwd ? take(4 * wn) : 0, oP = take(4 * (size_t)out * r),
-               oQ = take(4 * (size_t)r * in), oPG = take(4 * (size_t)out * r), ors = take(4 * out),
-               ocs = take(4 * in), otcn = take(4 * in), orn2 = take(8 * out), ocsq = take(8 * in),
-               otc = take(8 * in), owb = take(2 * wn), oxb = take(2 * (size_t)S * in),
-               odyb = bwd ? take(2 * (size_t)S * out) : 0, odyt = bwd ? take(2 * (size_t)out * b.ldt) : 0;
-  uint8_t* base = static_cast<uint8_t*>(scratch_get(c, kSlotMat, off, err));
-  if (!base) return false;
-  b.V = reinterpret_cast<float*>(base + oV);
-  b.G = bwd ? reinterpret_cast<float*>(base + oG) : nullptr;
-  b.P = reinterpret_cast<float*>(base + oP);
-  b.Q = reinterpret_cast<float*>(base + oQ);
-  b.PG = reinterpret_cast<float*>(base + oPG);
-  b.rs = reinterpret_cast<float*>(base + ors);
-  b.cs = reinterpret_cast<float*>(base + ocs);
-  b.tcn = reinterpret_cast<float*>(base + otcn);
-  b.rn2 = reinterpret_cast<double*>(base + orn2);
-  b.csq = reinterpret_cast<double*>(base + ocsq);
-  b.tc = reinterpret_cast<double*>(base + otc);
-  b.wb = reinterpret_cast<__nv_bfloat16*>(base + owb);
-  b.xb = reinterpret_cast<__nv_bfloat16*>(base + oxb);
-  b.dyb = bwd ? reinterpret_cast<__nv_bfloat16*>(base + odyb) : nullptr;
-  b.dyt = bwd ? reinterpret_cast<__nv_bfloat16*>(base + odyt) : nullptr;
-  return true;
-}
-
 // Slices of rows for the column kernels (blocks of `cols` columns): about four blocks per SM,
 // at least 16 rows a slice.
 int64_t col_rows_per(Ctx* c, int64_t out, int64_t in, int64_t cols) {
@@ -566,46 +433,6 @@ int64_t col_rows_per(Ctx* c, int64_t out, int64_t in, int64_t cols) {
   return rp < 16 ? 16 : rp;
 }
 constexpr int64_t kColBlockCols = 4 * kColThreads;
-
-// V, the row and column factors and W_eff (bf16 in b.wb; f32 into weff_f32 when not null).
-int mat_weight(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, MatBufs& b,
-               float* weff_f32, std::string& err) {
-  const int64_t in = w->in, out = w->out;
-  const int r = ad->rank;
-  const cudaStream_t st = c->stream;
-  const float* P = ad->B;
-  const float* Q = ad->A;
-  if (p.xs) {
-    ProfScope prof_(c, "mat.xs_prep");
-    mat_xs_prep_kernel<<<(unsigned)(2 * c->sm_count), 256, 0, st>>>(ad->U, ad->M, ad->V, out, in, r, b.P, b.Q);
-    if (check_launch("mat xs prep", err)) return 1;
-    P = b.P;
-    Q = b.Q;
-  }
-  {
-    ProfScope prof_(c, "mat.build");
-    mat_build_kernel<<<(unsigned)((out + kBdRows - 1) / kBdRows), kBdThreads, 0, st>>>(*w, P, Q, r, ad->scale, p.mr,
-                                                                                      b.V, b.rn2, b.rs);
-    if (check_launch("mat build", err)) return 1;
-  }
-  if (p.cols) {
-    ProfScope prof_(c, "mat.cols");
-    if (cudaMemsetAsync(b.csq, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
-    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
-    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
-                        kColThreads, 0, st>>>(b.V, nullptr, b.rs, out, in, rp, b.csq);
-    if (check_launch("mat colsum", err)) return 1;
-  }
-  {
-    ProfScope prof_(c, "mat.weff");
-    mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, nullptr, p.mc, out, in, b.cs, nullptr,
-                                                                   nullptr, 0);
-    if (check_launch("mat colfac", err)) return 1;
-    mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(b.V, b.rs, b.cs, out, in, b.wb, weff_f32);
-    if (check_launch("mat weff", err)) return 1;
-  }
-  return 0;
-}
 
 int mat_check(const sa3k_weight* w, const sa3k_mat_adapter* ad, int64_t S, MatPlan& p, std::string& err) {
   if (!parse_type(ad, p, err)) return 1;
@@ -620,82 +447,87 @@ int mat_check(const sa3k_weight* w, const sa3k_mat_adapter* ad, int64_t S, MatPl
   return 0;
 }
 
+// The target form of one call's adapter, its buffers and the call's scratch (x, dy as bf16, G,
+// the transposed dy, dD) carved from one context scratch slot.
+struct MatCall {
+  MatTarget t;
+  __nv_bfloat16 *xb = nullptr, *dyb = nullptr, *dyt = nullptr, *dDb = nullptr;
+  float* G = nullptr;
+  int64_t ldt = 0;
+};
+
+bool mat_prepare(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, const sa3k_mat_grads* g,
+                 int64_t S, bool bwd, MatCall& mc, std::string& err) {
+  MatTarget& t = mc.t;
+  t.xs = p.xs; t.rows = p.rows; t.cols = p.cols;
+  t.rank = ad->rank; t.s = ad->scale; t.w = w; t.in = w->in; t.out = w->out;
+  t.A = ad->A; t.B = ad->B; t.U = ad->U; t.Vb = ad->V; t.M = ad->M; t.mr = p.mr; t.mc = p.mc;
+  if (g) {
+    t.dA = g->dA; t.dB = g->dB; t.dM = g->dM;
+    t.dmr = p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr;
+    t.dmc = p.cols ? (p.rows ? g->dm_c : g->dm) : nullptr;
+  }
+  const int64_t in = w->in, out = w->out, wn = in * out;
+  mc.ldt = (S + 7) / 8 * 8;
+  auto al = [](size_t b) { return (b + 255) / 256 * 256; };
+  const size_t tb = al(mat_target_bytes(in, out, ad->rank)), xb = al(2 * (size_t)(S * in));
+  const size_t extra = bwd ? al(2 * (size_t)(S * out)) + al(2 * (size_t)(out * mc.ldt)) + al(2 * (size_t)wn) +
+                                 al(4 * (size_t)wn)
+                           : 0;
+  uint8_t* base = static_cast<uint8_t*>(scratch_get(c, kSlotMat, tb + xb + extra, err));
+  if (!base) return false;
+  mat_target_bind(t, base);
+  mc.xb = reinterpret_cast<__nv_bfloat16*>(base + tb);
+  if (bwd) {
+    uint8_t* q = base + tb + xb;
+    mc.dyb = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)(S * out));
+    mc.dyt = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)(out * mc.ldt));
+    mc.dDb = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)wn);
+    mc.G = reinterpret_cast<float*>(q);
+  }
+  return true;
+}
+
 int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& p, const float* bias, const float* x,
             const float* dy, int64_t S, float* y, float* dx, const sa3k_mat_grads* g, std::string& err) {
   const int64_t in = w->in, out = w->out;
   const int r = ad->rank;
   const cudaStream_t st = c->stream;
   const bool bwd = dy != nullptr;
-  MatBufs b;
-  if (!mat_alloc(c, S, in, out, r, bwd, b, err)) return 1;
-  if (mat_weight(c, w, ad, p, b, nullptr, err)) return 1;
-  if (k_cvt_bf16(c, x, S * in, b.xb, err)) return 1;
+  MatCall mc;
+  if (!mat_prepare(c, w, ad, p, g, S, bwd, mc, err)) return 1;
+  MatTarget& t = mc.t;
+  if (mat_target_build(c, t, nullptr, err)) return 1;
+  if (k_cvt_bf16(c, x, S * in, mc.xb, err)) return 1;
   if (y) {
     GemmDesc d;   // y = x W_eff^T + bias
     d.M = (int)S; d.N = (int)out; d.K = (int)in;
-    d.a = b.xb; d.lda = in;
-    d.bsrc = kB_BF16_KMAJOR; d.b = b.wb; d.ldb = in;
+    d.a = mc.xb; d.lda = in;
+    d.bsrc = kB_BF16_KMAJOR; d.b = t.wb; d.ldb = in;
     d.col_bias = bias;
     d.out = y; d.ldo = out;
     d.name = "mat.fwd";
     if (gemm(c, d, err)) return 1;
   }
   if (!bwd) return 0;
-  if (k_cvt_bf16(c, dy, S * out, b.dyb, err)) return 1;
+  // the gradients are written: clear them, then the target pass adds into them
+  auto zero = [&](float* q, int64_t n) {
+    return !q || cudaMemsetAsync(q, 0, sizeof(float) * (size_t)n, st) == cudaSuccess;
+  };
+  if (!zero(t.dA, (int64_t)r * in) || !zero(t.dB, out * r) || !zero(t.dM, (int64_t)r * r) || !zero(t.dmr, out) ||
+      !zero(t.dmc, in))
+    return check_launch("memset", err);
+  if (k_cvt_bf16(c, dy, S * out, mc.dyb, err)) return 1;
   if (dx) {
     GemmDesc d;   // dx = dy W_eff
     d.M = (int)S; d.N = (int)in; d.K = (int)out;
-    d.a = b.dyb; d.lda = out;
-    d.bsrc = kB_BF16_MNMAJOR; d.b = b.wb; d.ldb = in;
+    d.a = mc.dyb; d.lda = out;
+    d.bsrc = kB_BF16_MNMAJOR; d.b = t.wb; d.ldb = in;
     d.out = dx; d.ldo = in;
     d.name = "mat.dx";
     if (gemm(c, d, err)) return 1;
   }
-  {
-    ProfScope prof_(c, "mat.transpose");
-    transpose_bf16_kernel<<<dim3((unsigned)((S + 31) / 32), (unsigned)((out + 31) / 32)), dim3(32, 8), 0, st>>>(
-        dy, S, out, b.dyt, b.ldt);
-    if (check_launch("mat transpose", err)) return 1;
-  }
-  {
-    GemmDesc d;   // G = dy^T x  [out][in], K = tokens
-    d.M = (int)out; d.N = (int)in; d.K = (int)S;
-    d.a = b.dyt; d.lda = b.ldt;
-    d.bsrc = kB_BF16_MNMAJOR; d.b = b.xb; d.ldb = in;
-    d.out = b.G; d.ldo = in;
-    d.name = "mat.dW";
-    if (gemm(c, d, err)) return 1;
-  }
-  const float* Q = p.xs ? b.Q : ad->A;
-  if (p.cols) {
-    ProfScope prof_(c, "mat.cols_bwd");
-    if (cudaMemsetAsync(b.tc, 0, sizeof(double) * in, st) != cudaSuccess) return check_launch("memset", err);
-    const int64_t rp = col_rows_per(c, out, in, kColBlockCols);
-    mat_colsum_kernel<<<dim3((unsigned)((in + kColBlockCols - 1) / kColBlockCols), (unsigned)((out + rp - 1) / rp)),
-                        kColThreads, 0, st>>>(b.V, b.G, b.rs, out, in, rp, b.tc);
-    if (check_launch("mat colsum bwd", err)) return 1;
-    mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(b.csq, b.tc, p.mc, out, in, b.cs, b.tcn,
-                                                                   p.rows ? g->dm_c : g->dm, 0);
-    if (check_launch("mat colfac bwd", err)) return 1;
-  }
-  {
-    ProfScope prof_(c, "mat.rows_bwd");
-    mat_rowbwd_kernel<false><<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
-        b.G, b.V, b.rs, b.rn2, b.cs, b.tcn, Q, out, in, r, ad->scale, p.rows ? 1 : 0, p.cols ? 1 : 0,
-        p.rows ? (p.cols ? g->dm_r : g->dm) : nullptr, p.xs ? b.PG : g->dB, 0, 0, nullptr);
-    if (check_launch("mat rows bwd", err)) return 1;
-  }
-  if (p.xs) {
-    ProfScope prof_(c, "mat.dM");
-    mat_dm_xs_kernel<<<(unsigned)(r * r), 256, 0, st>>>(ad->U, b.PG, out, r, g->dM, 0);
-    return check_launch("mat dM", err);
-  }
-  ProfScope prof_(c, "mat.dA");
-  if (cudaMemsetAsync(g->dA, 0, sizeof(float) * (size_t)r * in, st) != cudaSuccess) return check_launch("memset", err);
-  const int64_t rp = col_rows_per(c, out, in, 256);
-  mat_da_kernel<<<dim3((unsigned)((in + 255) / 256), (unsigned)((out + rp - 1) / rp)), 256, 0, st>>>(
-      b.G, ad->B, out, in, r, rp, g->dA);
-  return check_launch("mat dA", err);
+  return mat_target_backward(c, t, mc.dyb, S, mc.xb, mc.G, mc.dyt, mc.ldt, mc.dDb, err);
 }
 
 int mfail(char* err, int len, const std::string& msg) {
@@ -735,7 +567,7 @@ void mat_target_bind(MatTarget& t, void* mem) {
   t.Btb = reinterpret_cast<__nv_bfloat16*>(take(2 * (size_t)t.rank * t.out));
 }
 
-int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
+int mat_target_build(Ctx* c, MatTarget& t, float* weff_f32, std::string& err) {
   const int64_t in = t.in, out = t.out;
   const int r = t.rank;
   const cudaStream_t st = c->stream;
@@ -771,7 +603,7 @@ int mat_target_build(Ctx* c, MatTarget& t, std::string& err) {
   mat_colfac_kernel<<<(unsigned)((in + 255) / 256), 256, 0, st>>>(t.csq, nullptr, t.cols ? t.mc : nullptr, out, in,
                                                                  t.cs, nullptr, nullptr, 0);
   if (check_launch("mat colfac", err)) return 1;
-  mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(t.V, t.rs, t.cs, out, in, t.wb, nullptr);
+  mat_weff_kernel<<<(unsigned)(4 * c->sm_count), 256, 0, st>>>(t.V, t.rs, t.cs, out, in, t.wb, weff_f32);
   if (check_launch("mat weff", err)) return 1;
   mat_pack_kernel<<<(unsigned)(c->sm_count), 256, 0, st>>>(Q, t.xs ? nullptr : t.B, out, in, r, t.Qb, t.Btb);
   return check_launch("mat pack", err);
@@ -782,8 +614,8 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   const int64_t in = t.in, out = t.out;
   const int r = t.rank;
   const cudaStream_t st = c->stream;
-  if (ldt < M || ldt % 8 || out % 2) {
-    err = "mat backward: transposed gradient pitch (or an odd output width)";
+  if (ldt < M || ldt % 8) {
+    err = "mat backward: transposed gradient pitch";
     return 1;
   }
   {
@@ -813,9 +645,8 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   }
   {
     ProfScope prof_(c, "mat.rows_bwd");
-    mat_rowbwd_kernel<true><<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
-        G, t.V, t.rs, t.rn2, t.cs, t.tcn, nullptr, out, in, r, t.s, t.rows ? 1 : 0, t.cols ? 1 : 0,
-        t.rows ? t.dmr : nullptr, nullptr, 0, 1, dDb);
+    mat_rowbwd_kernel<<<(unsigned)((out + kRbRows - 1) / kRbRows), kRbThreads, 0, st>>>(
+        G, t.V, t.rs, t.rn2, t.cs, t.tcn, out, in, t.s, t.rows ? 1 : 0, t.cols ? 1 : 0, t.rows ? t.dmr : nullptr, dDb);
     if (check_launch("mat rows bwd", err)) return 1;
   }
   if (t.xs && cudaMemsetAsync(t.PG, 0, sizeof(float) * (size_t)out * r, st) != cudaSuccess)
@@ -865,8 +696,8 @@ int sa3k_mat_effective_weight(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_ma
   if (mat_check(w, ad, 1, p, e)) return mfail(err, err_len, e);
   Ctx* c = &ctx->c;
   cudaSetDevice(c->device);
-  MatBufs b;
-  if (!mat_alloc(c, 1, w->w.in, w->w.out, ad->rank, false, b, e) || mat_weight(c, &w->w, ad, p, b, weff, e))
+  MatCall mc;
+  if (!mat_prepare(c, &w->w, ad, p, nullptr, 1, false, mc, e) || mat_target_build(c, mc.t, weff, e))
     return mfail(err, err_len, e);
   return 0;
 }

@@ -32,8 +32,9 @@ struct MatTarget {
 
 size_t mat_target_bytes(int64_t in, int64_t out, int rank);
 void mat_target_bind(MatTarget& t, void* mem);
-// V, the row / column factors and W_eff (t.wb) from the current parameters.
-int mat_target_build(Ctx* c, MatTarget& t, std::string& err);
+// V, the row / column factors and W_eff (t.wb; also f32 into weff_f32 when not null) from the
+// current parameters.
+int mat_target_build(Ctx* c, MatTarget& t, float* weff_f32, std::string& err);
 // The weight gradient of one backward: G = dz^T x (dz [M][out] bf16, x [M][in] bf16, K = M) into
 // G [out][in] f32 scratch (dzt: [out][ldt] bf16 scratch, ldt >= M, a multiple of 8), then the
 // normalisation backward into dD = s dV (dDb: [out][in] bf16 scratch) and the rank-r GEMMs on dD;

@@ -157,9 +157,9 @@ def mat_case(a):
         E = n * k
         code = {"q8_0": 1.0 + 4.0 / 32, "q4_k": 0.5 + 8.0 / 32}[a.qtype]
         work = {"mat.build": (E * (code + 4), "B"), "mat.cols": (E * 4, "B"), "mat.weff": (E * 6, "B"),
-                "mat.transpose": (m * n * 6, "B"), "mat.cols_bwd": (E * 8, "B"), "mat.rows_bwd": (E * 12, "B"),
-                "mat.dA": (E * 4, "B"), "mat.fwd": (2.0 * m * n * k, "F"), "mat.dx": (2.0 * m * n * k, "F"),
-                "mat.dW": (2.0 * m * n * k, "F")}
+                "mat.transpose": (m * n * 4, "B"), "mat.cols_bwd": (E * 8, "B"), "mat.rows_bwd": (E * 10, "B"),
+                "mat.dA": (2.0 * E * r, "F"), "mat.dB": (2.0 * E * r, "F"), "mat.fwd": (2.0 * m * n * k, "F"),
+                "mat.dx": (2.0 * m * n * k, "F"), "mat.dW": (2.0 * m * n * k, "F")}
         total = 0.0
         print(f"mat {a.type} {a.qtype} tokens {m}, in {k}, out {n}, rank {r}")
         for name, (cnt, ms) in sorted(ctx.profile_read().items()):
