@@ -272,7 +272,9 @@ int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim
  * first call on each device looks up that array's address (cudaGetSymbolAddress, which may load
  * the library's device code); make that first call before capturing a stream.  All calls on one
  * device share the array, so two calls in flight at the same time (other streams, other
- * contexts, other threads) race: serialise them.  Same arguments and results as
+ * contexts, other threads) race: serialise them.  The looked-up address is kept for the life of
+ * the process, so resetting a device (cudaDeviceReset, or another library resetting the primary
+ * context) while this library is loaded is not supported.  Same arguments and results as
  * sa3k_attention_bwd. */
 int sa3k_attention_bwd_noalloc(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim,
                                float scale, int window, const sa3k_tensor4* q,

@@ -418,21 +418,17 @@ __global__ void __launch_bounds__(NT) attn_bwd_dkdv_kernel(const AttnArgs p) {
 
 constexpr int kSmemFwd = 8192 * 5, kSmemDq = 8192 * 6, kSmemDkdv = 8192 * 6 + 4 * TQ * 4;
 
-static int set_attrs(std::string& err) {
-  static bool done = false;
-  if (done) return 0;
-  if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemFwd) != cudaSuccess ||
-      cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDq) != cudaSuccess ||
-      cudaFuncSetAttribute(attn_bwd_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemDkdv) != cudaSuccess)
-    return check_launch("attention smem attributes", err);
-  done = true;
-  return 0;
+static int set_attrs(int device, std::string& err) {
+  const char* what = "attention smem attributes";
+  return smem_attr(reinterpret_cast<const void*>(attn_fwd_kernel), kSmemFwd, device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_bwd_dq_kernel), kSmemDq, device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_bwd_dkdv_kernel), kSmemDkdv, device, what, err);
 }
 
 int attn_forward(Ctx* c, const AttnArgs& a, std::string& err) {
   if (a.head_dim != HD) { err = "attention: head_dim must be 64"; return 1; }
   if (c->attn_tc && attn_tc_supported(a)) return attn_tc_forward(c, a, err);
-  if (set_attrs(err)) return 1;
+  if (set_attrs(c->device, err)) return 1;
   ProfScope prof_(c, "attn.fwd");
   dim3 grid((unsigned)((a.Sq + TQ - 1) / TQ), (unsigned)(a.B * a.H));
   launch_pdl(c, attn_fwd_kernel, grid, NT, kSmemFwd, a);
@@ -443,7 +439,7 @@ int attn_backward(Ctx* c, const AttnArgs& a, bool want_dkdv, std::string& err) {
   if (a.head_dim != HD) { err = "attention: head_dim must be 64"; return 1; }
   // the tcgen05 dq pass forms D = rowsum(dO o O) itself
   if (c->attn_tc && attn_tc_supported(a)) return attn_tc_grads(c, a, want_dkdv, err);
-  if (set_attrs(err)) return 1;
+  if (set_attrs(c->device, err)) return 1;
   {
     ProfScope prof_(c, "attn.bwd_pre");
     const long rows = (long)a.B * a.H * a.Sq;

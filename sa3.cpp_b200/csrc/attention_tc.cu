@@ -1078,15 +1078,11 @@ TcArgs tc_args(const AttnArgs& p) {
   return a;
 }
 
-int set_tc_attrs(std::string& err) {
-  static bool done = false;
-  if (done) return 0;
-  if (cudaFuncSetAttribute(attn_tc_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_req(F_SMEM)) != cudaSuccess ||
-      cudaFuncSetAttribute(attn_tc_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_req(Q_SMEM)) != cudaSuccess ||
-      cudaFuncSetAttribute(attn_tc_dkdv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_req(KV_SMEM)) != cudaSuccess)
-    return check_launch("attention tc smem attributes", err);
-  done = true;
-  return 0;
+int set_tc_attrs(int device, std::string& err) {
+  const char* what = "attention tc smem attributes";
+  return smem_attr(reinterpret_cast<const void*>(attn_tc_fwd_kernel), smem_req(F_SMEM), device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_tc_dq_kernel), smem_req(Q_SMEM), device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_tc_dkdv_kernel), smem_req(KV_SMEM), device, what, err);
 }
 
 }  // namespace
@@ -1104,7 +1100,7 @@ bool attn_tc_supported(const AttnArgs& p) {
 }
 
 int attn_tc_forward(Ctx* c, const AttnArgs& p, std::string& err) {
-  if (set_tc_attrs(err)) return 1;
+  if (set_tc_attrs(c->device, err)) return 1;
   TcArgs a = tc_args(p);
   a.err = c->d_err;
   CUtensorMap mq, mk, mv;
@@ -1119,7 +1115,7 @@ int attn_tc_forward(Ctx* c, const AttnArgs& p, std::string& err) {
 }
 
 int attn_tc_grads(Ctx* c, const AttnArgs& p, bool want_dkdv, std::string& err) {
-  if (set_tc_attrs(err)) return 1;
+  if (set_tc_attrs(c->device, err)) return 1;
   TcArgs a = tc_args(p);
   a.err = c->d_err;
   {

@@ -319,12 +319,7 @@ void r16_group_free(R16Group& g) {
 
 int r16_group_run(Ctx* c, const R16Group& g, const char* name, std::string& err) {
   if (!g.table || g.nitems == 0) return 0;
-  static bool attr = false;
-  if (!attr) {
-    if (cudaFuncSetAttribute(r16_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kDyn) != cudaSuccess)
-      return check_launch("r16 smem attribute", err);
-    attr = true;
-  }
+  if (smem_attr(reinterpret_cast<const void*>(r16_group_kernel), kDyn, c->device, "r16 smem attribute", err)) return 1;
   const int grid = std::min<long>(g.nitems, (long)c->sm_count);
   ProfScope prof_(c, name);
   launch_pdl(c, r16_group_kernel, grid, kThreads, kDyn, static_cast<const R16Problem*>(g.table), g.nprob, g.nitems,

@@ -3,8 +3,10 @@
 #include "gemm_tc2.cuh"
 #include "sa3k_internal.h"
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
+#include <set>
 
 namespace sa3k {
 
@@ -20,6 +22,17 @@ PFN_encodeTiled encode_tiled_fn(std::string& err) {
   });
   if (!fn) err = "cuTensorMapEncodeTiled is unavailable (no CUDA driver)";
   return fn;
+}
+
+int smem_attr(const void* kern, int bytes, int device, const char* what, std::string& err) {
+  static std::mutex mu;
+  static std::set<std::pair<const void*, int>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count({kern, device})) return 0;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return check_launch(what, err);
+  done.insert({kern, device});
+  return 0;
 }
 
 // 2-D tensor map over a row-major [outer][inner] array with `row_bytes` between rows.
@@ -109,12 +122,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   using R = GemmRoles<BMODE>;
   auto kern = gemm_tc_kernel<BN, STAGES, BMODE, A_MN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN) != cudaSuccess)
-      return check_launch("gemm smem attribute", err);
-    attr_set = true;
-  }
+  if (smem_attr(reinterpret_cast<const void*>(kern), L::DYN, c->device, "gemm smem attribute", err)) return 1;
   const long tiles = (long)((d.M + kBM - 1) / kBM) * ((d.N + BN - 1) / BN);
   GemmArgs a = args;
   // split-K when the output has too few tiles to fill the GPU and K is long
@@ -183,10 +191,10 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
   using L = Gemm2Smem<BN, STAGES>;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   auto kern = gemm_tc2_kernel<BN, STAGES, BMODE>;
-  static int max_clusters = 0;
-  if (!max_clusters) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN) != cudaSuccess)
-      return check_launch("gemm pair smem attribute", err);
+  if (smem_attr(reinterpret_cast<const void*>(kern), L::DYN, c->device, "gemm pair smem attribute", err)) return 1;
+  // (the cluster occupancy is a property of the kernel and the sm_100 part, the same on every device)
+  static std::atomic<int> max_clusters{0};
+  if (!max_clusters.load()) {
     cudaLaunchConfig_t q = {};
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeClusterDimension;
@@ -201,7 +209,7 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
       cudaGetLastError();
       n = c->sm_count / 2;
     }
-    max_clusters = n;
+    max_clusters.store(n);
   }
   GemmArgs a = args;
   a.splits = 1;

@@ -440,7 +440,7 @@ int mat_check(const sa3k_weight* w, const sa3k_mat_adapter* ad, int64_t S, MatPl
     err = "in must be a multiple of 64";
     return 1;
   }
-  if (S < 0) {
+  if (S <= 0) {
     err = "S must be positive";
     return 1;
   }

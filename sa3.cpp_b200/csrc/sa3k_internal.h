@@ -116,6 +116,11 @@ inline cudaError_t launch_pdl(Ctx* c, void (*kern)(KArgs...), dim3 grid, dim3 bl
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
+// cudaFuncAttributeMaxDynamicSharedMemorySize of `kern` on `device` (the current device), set once
+// per (kernel, device): the attribute is per device, and contexts may live on several devices of
+// one process and be driven from several threads.
+int smem_attr(const void* kern, int bytes, int device, const char* what, std::string& err);
+
 inline int check_launch(const char* what, std::string& err) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
