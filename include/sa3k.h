@@ -48,24 +48,34 @@ void sa3k_ctx_destroy(sa3k_ctx* ctx);
 int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len);
 
 /* Context options (sa3k_ctx_set_option).  No counterpart in the reference.
- *   SA3K_OPT_WEIGHT_BF16_CACHE  1 (default): a Q8_0 / Q4_K weight uploaded afterwards also keeps
- *       a bf16 operand copy, made once by the bit-exact dequantizer (the frozen base never
- *       changes, so the tensor cores then read bf16 tiles directly).  0: codes + scales only.
+ *   SA3K_OPT_WEIGHT_F16_CACHE  1 (default): a Q8_0 / Q4_K weight uploaded afterwards also keeps
+ *       an IEEE half (f16) operand copy, made once by the bit-exact dequantizer (the frozen base
+ *       never changes, so the tensor cores then read f16 tiles directly).  0: codes + scales only.
  *   SA3K_OPT_SMEM_DEQUANT  1: GEMMs over quantized weights dequantize each TMA-loaded tile in
- *       shared memory even when a bf16 copy exists.  0 (default): use the copy when present.
- * Both paths round the same f32 dequantized value once to bf16, so results are identical. */
-#define SA3K_OPT_WEIGHT_BF16_CACHE 1
+ *       shared memory even when an f16 copy exists.  0 (default): use the copy when present.
+ * Both paths round the same f32 dequantized value once to f16, so results are identical.
+ *
+ * Operand type.  Every tensor-core contraction of the library (the GEMM engine, the rank-16
+ * GEMMs, attention) reads IEEE half operands (11-bit significand) with f32 accumulation.  Against
+ * bf16 (8-bit significand) at the same tensor-core rate this is 8x less rounding of the frozen
+ * base weights, whose rounding error is the same for every token and so does not average out of
+ * the adapter gradients.  The f16 range (largest 65504, normal down to 6.1e-5) suits normalized
+ * activations; gradients are carried scaled: the DiT step multiplies its loss gradient by a
+ * power of two and divides the adapter gradients by it again (exact), and the component
+ * backward calls take the upstream gradient as given (callers with very small gradients scale
+ * them the same way). */
+#define SA3K_OPT_WEIGHT_F16_CACHE 1
 #define SA3K_OPT_SMEM_DEQUANT 2
 /* SA3K_OPT_GEMM_TILE_N  0 (default): the N tile of the large GEMMs comes from a wave-count cost
  *       model; 128, 192 or 256 fixes it (a tuning knob; results do not depend on it). */
 #define SA3K_OPT_GEMM_TILE_N 3
-/* SA3K_OPT_GEMM_PAIR  1 (default): bf16-operand GEMMs with at least 256 rows and enough output
+/* SA3K_OPT_GEMM_PAIR  1 (default): f16-operand GEMMs with at least 256 rows and enough output
  *       tiles run on CTA pairs (tcgen05 cta_group::2, 256-row tiles); 0: one CTA per tile always;
  *       2: CTA pairs wherever they apply (a tuning knob; with SA3K_OPT_GEMM_TILE_N 192 the pair
  *       tiles are 256 x 192).  Results are identical either way (same per-element summation order). */
 #define SA3K_OPT_GEMM_PAIR 4
 /* SA3K_OPT_ATTN_TC  1 (default): attention on the tcgen05 tensor cores (TMEM accumulators, P and
- *       dS fed back from TMEM); 0: the mma.sync kernels.  Both compute in bf16 with f32
+ *       dS fed back from TMEM); 0: the mma.sync kernels.  Both compute in f16 with f32
  *       accumulation; results agree to rounding. */
 #define SA3K_OPT_ATTN_TC 5
 /* SA3K_OPT_PDL  1 (default): kernels launched outside a stream capture use programmatic
@@ -245,7 +255,7 @@ typedef struct sa3k_tensor4 {
   int64_t batch_stride, head_stride, row_stride;
 } sa3k_tensor4;
 
-/* o = softmax(scale * q k^T [+ band mask]) v per (batch, head), head_dim 64; q, k, v, o bf16.
+/* o = softmax(scale * q k^T [+ band mask]) v per (batch, head), head_dim 64; q, k, v, o f16 (IEEE half).
  * window < 0: dense (the DiT's sdpa); window >= 0: keys with |i - j| <= window only (the banded
  * attention of BASELINE config 3).  lse [B*H][Sq] (f32, log2 units) is kept for the backward.
  * Replaces nn::sdpa (src/nn.h:135-144) and the band of attn_sliding (src/nn.h:79-100). */
@@ -254,7 +264,7 @@ int sa3k_attention_fwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim
                        const sa3k_tensor4* v, const sa3k_tensor4* o, float* lse, char* err,
                        int err_len);
 
-/* Backward of sa3k_attention_fwd for upstream dO (bf16): dq, dk, dv (f32; dk and dv may be NULL
+/* Backward of sa3k_attention_fwd for upstream dO (f16): dq, dk, dv (f32; dk and dv may be NULL
  * for a frozen key/value source such as the cross-attention context).  Replaces the
  * SOFT_MAX_BACK / OUT_PROD chain ggml derives for nn::sdpa. */
 int sa3k_attention_bwd(sa3k_ctx* ctx, int B, int H, int Sq, int Sk, int head_dim, float scale,
@@ -291,13 +301,13 @@ typedef struct sa3k_head_slice {
   float* rstd;          /* [T][H] saved 1/rms per (token, head) when gamma != NULL          */
 } sa3k_head_slice;
 
-/* out[T][ncols] (bf16) = per-head prepared slices of y[T][ncols] (f32): RMSNorm over each head's
+/* out[T][ncols] (f16) = per-head prepared slices of y[T][ncols] (f32): RMSNorm over each head's
  * 64 values with gamma (eps), then NeoX RoPE of the first `rot` (32 or 64) dims at position
  * (token index mod tokens_per_sample), base `rope_base`.  Replaces the qknorm + rope_neox of
  * dit_block (src/dit.h:195, 209-217; src/nn.h:53-59). */
 int sa3k_head_prep_fwd(sa3k_ctx* ctx, const float* y, int T, int ncols, int H,
                        const sa3k_head_slice* slices, int nslices, int tokens_per_sample, float eps,
-                       int rot, float rope_base, void* out_bf16, char* err, int err_len);
+                       int rot, float rope_base, void* out_f16, char* err, int err_len);
 
 /* Backward of one slice: g[T][H*64] (f32, row stride g_ld) is the gradient w.r.t. the prepared
  * slice; writes the gradient w.r.t. y into that slice of dy[T][ncols] (f32). */

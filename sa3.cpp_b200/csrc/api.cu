@@ -74,12 +74,12 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (dora && !ad->base_norm_sq) { err = "dora adapter needs base_norm_sq"; return 1; }
   if (bwd && !fwd && dora && !y_in) { err = "dora backward needs the forward output y"; return 1; }
   const int64_t s_pad = pad64(S);
-  __nv_bfloat16* x_bf;
-  if (!get(c, kS_XBF, S * in, x_bf, err)) return 1;
-  if (k_cvt_bf16(c, x, S * in, x_bf, err)) return 1;
+  __half* x_h;
+  if (!get(c, kS_XBF, S * in, x_h, err)) return 1;
+  if (k_cvt_f16(c, x, S * in, x_h, err)) return 1;
 
   AdapterPrep prep;
-  __nv_bfloat16* ut = nullptr;
+  __half* ut = nullptr;
   if (adapter) {
     prep.rank = ad->rank; prep.in = in; prep.out = out; prep.s = ad->scale;
     prep.A = ad->A; prep.B = ad->B; prep.m = dora ? ad->magnitude : nullptr; prep.bns = ad->base_norm_sq;
@@ -93,18 +93,18 @@ static int linear_run(Ctx* c, const Weight* w, const sa3k_adapter* ad, const flo
   if (fwd || (bwd && adapter)) {
     // the backward needs u^T, which the forward produces; a backward-only call recomputes it
     LinearFwd f;
-    f.w = w; f.ad = adapter ? &prep : nullptr; f.bias = bias; f.x_bf = x_bf; f.M = S;
+    f.w = w; f.ad = adapter ? &prep : nullptr; f.bias = bias; f.x_h = x_h; f.M = S;
     f.y = y_out; f.ut = ut; f.ut_ld = s_pad;
     if (!fwd) {
       // u only (the main GEMM is skipped without an output)
-      if (lora_u(c, x_bf, S, in, prep, ut, s_pad, err)) return 1;
+      if (lora_u(c, x_h, S, in, prep, ut, s_pad, err)) return 1;
     } else if (linear_forward(c, f, err)) {
       return 1;
     }
   }
   if (!bwd) return 0;
   LinearBwd b;
-  b.w = w; b.ad = adapter ? &prep : nullptr; b.bias = bias; b.x_bf = x_bf; b.y = fwd ? y_out : y_in; b.dy = dy;
+  b.w = w; b.ad = adapter ? &prep : nullptr; b.bias = bias; b.x_h = x_h; b.y = fwd ? y_out : y_in; b.dy = dy;
   b.M = S; b.ut = ut; b.ut_ld = s_pad;
   b.dx = dx; b.dx_accumulate = accumulate;
   b.dA = dA; b.dB = dB; b.dm = dm; b.grad_accumulate = accumulate;
@@ -245,7 +245,7 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
   if (!ctx) return fill_err(err, err_len, "ctx is NULL");
   ++ctx->c.gen;
   switch (option) {
-    case SA3K_OPT_WEIGHT_BF16_CACHE: ctx->c.weight_cache = value != 0; return 0;
+    case SA3K_OPT_WEIGHT_F16_CACHE: ctx->c.weight_cache = value != 0; return 0;
     case SA3K_OPT_SMEM_DEQUANT: ctx->c.smem_dequant = value != 0; return 0;
     case SA3K_OPT_GEMM_TILE_N:
       if (value != 0 && value != 128 && value != 192 && value != 256)
@@ -340,7 +340,7 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
     if (w.raw) cudaFree(w.raw);
     if (w.codes) cudaFree(w.codes);
     if (w.scales) cudaFree(w.scales);
-    if (w.bf16) cudaFree(w.bf16);
+    if (w.f16) cudaFree(w.f16);
     delete h;
     cudaGetLastError();
     return fill_err(err, err_len, msg);
@@ -357,12 +357,12 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
         cudaMalloc(&w.scales, (size_t)(in / 32 * out * 8)) != cudaSuccess)
       return fail("out of device memory (weight)");
   } else {
-    if (cudaMalloc(&w.bf16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight)");
+    if (cudaMalloc(&w.f16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight)");
   }
   if (weight_repack(&ctx->c, &w, e)) return fail(e);
   if ((type == kTypeQ8_0 || type == kTypeQ4_K) && ctx->c.weight_cache) {
-    if (cudaMalloc(&w.bf16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight cache)");
-    if (weight_cache_bf16(&ctx->c, &w, e)) return fail(e);
+    if (cudaMalloc(&w.f16, (size_t)(in * out * 2)) != cudaSuccess) return fail("out of device memory (weight cache)");
+    if (weight_cache_f16(&ctx->c, &w, e)) return fail(e);
   }
   if (cudaStreamSynchronize(ctx->c.stream) != cudaSuccess) return fail("weight repack failed");
   if (type == kTypeQ8_0 || type == kTypeQ4_K) {   // codes + scales carry every bit of the blocks
@@ -380,7 +380,7 @@ void sa3k_weight_free(sa3k_weight* h) {
   if (w.raw) cudaFree(w.raw);
   if (w.codes) cudaFree(w.codes);
   if (w.scales) cudaFree(w.scales);
-  if (w.bf16) cudaFree(w.bf16);
+  if (w.f16) cudaFree(w.f16);
   delete h;
 }
 
@@ -485,8 +485,8 @@ int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_ada
   return 0;
 }
 
-static void set4(const sa3k_tensor4* t, const __nv_bfloat16*& p, long& sb, long& sh, long& ld) {
-  p = static_cast<const __nv_bfloat16*>(t->data);
+static void set4(const sa3k_tensor4* t, const __half*& p, long& sb, long& sh, long& ld) {
+  p = static_cast<const __half*>(t->data);
   sb = (long)t->batch_stride;
   sh = (long)t->head_stride;
   ld = (long)t->row_stride;
@@ -501,7 +501,7 @@ static int attn_args(int B, int H, int Sq, int Sk, int head_dim, float scale, in
   set4(q, a.q, a.q_sb, a.q_sh, a.q_ld);
   set4(k, a.k, a.k_sb, a.k_sh, a.k_ld);
   set4(v, a.v, a.v_sb, a.v_sh, a.v_ld);
-  a.o = static_cast<__nv_bfloat16*>(o->data);
+  a.o = static_cast<__half*>(o->data);
   a.o_sb = (long)o->batch_stride; a.o_sh = (long)o->head_stride; a.o_ld = (long)o->row_stride;
   for (long st : {a.q_ld, a.k_ld, a.v_ld, a.o_ld})
     if (st % 8) { err = "attention rows must be 16-byte aligned (row_stride % 8 == 0)"; return 1; }
@@ -623,7 +623,7 @@ int sa3k_head_prep_fwd(sa3k_ctx* ctx, const float* y, int T, int ncols, int H, c
   }
   std::string e;
   if (k_head_prep_fwd(&ctx->c, y, T, ncols, H, hs, nslices, tps, eps, rot, rope_base,
-                      static_cast<__nv_bfloat16*>(out), e))
+                      static_cast<__half*>(out), e))
     return fill_err(err, err_len, e);
   return 0;
 }

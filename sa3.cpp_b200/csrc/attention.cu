@@ -11,8 +11,8 @@
 //   dq pass   (one CTA per 64 queries, loop over keys):  dQ = scale * dS K
 //   dkdv pass (one CTA per 64 keys, loop over queries):  dV = P^T dO,  dK = scale * dS^T Q
 // with dS = P o (dP - D), dP = dO V^T, D = rowsum(dO o O).
-// Tiles are bf16 in 128-byte rows with the 16-byte chunks XOR-swizzled by (row & 7); the
-// products run on mma.sync m16n8k16 (bf16 in, f32 accumulate).
+// Tiles are f16 in 128-byte rows with the 16-byte chunks XOR-swizzled by (row & 7); the
+// products run on mma.sync m16n8k16 (f16 in, f32 accumulate).
 //
 // Tensor addressing: element (b, h, s, d) of q is at q + b*sb + h*sh + s*ld + d, so q / k / v
 // can be read straight out of the token-major qkv buffer [B][S][3*dim] and O / dO live in the
@@ -50,14 +50,14 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
 }
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// [64 rows][64 bf16] tile from rows row0.. of a strided tensor (rows >= nrows read as zero).
-__device__ __forceinline__ void load_tile(uint32_t sbase, const __nv_bfloat16* g, long ld, int row0, int nrows,
+// [64 rows][64 f16] tile from rows row0.. of a strided tensor (rows >= nrows read as zero).
+__device__ __forceinline__ void load_tile(uint32_t sbase, const __half* g, long ld, int row0, int nrows,
                                           int tid) {
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -102,14 +102,14 @@ __device__ __forceinline__ void mma_ab(float (&acc)[8][4], const uint32_t (&a)[4
   }
 }
 
-// f32 accumulator fragments [16 x 64] -> bf16 A fragments (the FA2 register reuse).
+// f32 accumulator fragments [16 x 64] -> f16 A fragments (the FA2 register reuse).
 __device__ __forceinline__ void acc_to_a(uint32_t (&a)[4][4], const float (&c)[8][4]) {
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
-    a[ks][0] = pack_bf16x2(c[2 * ks][0], c[2 * ks][1]);
-    a[ks][1] = pack_bf16x2(c[2 * ks][2], c[2 * ks][3]);
-    a[ks][2] = pack_bf16x2(c[2 * ks + 1][0], c[2 * ks + 1][1]);
-    a[ks][3] = pack_bf16x2(c[2 * ks + 1][2], c[2 * ks + 1][3]);
+    a[ks][0] = pack_f16x2(c[2 * ks][0], c[2 * ks][1]);
+    a[ks][1] = pack_f16x2(c[2 * ks][2], c[2 * ks][3]);
+    a[ks][2] = pack_f16x2(c[2 * ks + 1][0], c[2 * ks + 1][1]);
+    a[ks][3] = pack_f16x2(c[2 * ks + 1][2], c[2 * ks + 1][3]);
   }
 }
 
@@ -143,9 +143,9 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const AttnArgs p) {
   const int g = lane >> 2, t4 = lane & 3;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int q0 = blockIdx.x * TQ;
-  const __nv_bfloat16* qg = p.q + b * p.q_sb + h * p.q_sh;
-  const __nv_bfloat16* kg = p.k + b * p.k_sb + h * p.k_sh;
-  const __nv_bfloat16* vg = p.v + b * p.v_sb + h * p.v_sh;
+  const __half* qg = p.q + b * p.q_sb + h * p.q_sh;
+  const __half* kg = p.k + b * p.k_sb + h * p.k_sh;
+  const __half* vg = p.v + b * p.v_sb + h * p.v_sh;
   const uint32_t sQ = smem_u32(sm), sK = sQ + 8192, sV = sQ + 3 * 8192;
   int kt0, kt1;
   key_range(q0, p.Sk, p.window, kt0, kt1);
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const AttnArgs p) {
     l[r] += __shfl_xor_sync(0xffffffffu, l[r], 1);
     l[r] += __shfl_xor_sync(0xffffffffu, l[r], 2);
   }
-  __nv_bfloat16* og = p.o + b * p.o_sb + h * p.o_sh;
+  __half* og = p.o + b * p.o_sb + h * p.o_sh;
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int qi = qr[r];
@@ -227,7 +227,7 @@ __global__ void __launch_bounds__(NT) attn_fwd_kernel(const AttnArgs p) {
     const float inv = l[r] > 0.f ? 1.f / l[r] : 0.f;
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
-      const uint32_t v2 = pack_bf16x2(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
+      const uint32_t v2 = pack_f16x2(o[nt][2 * r] * inv, o[nt][2 * r + 1] * inv);
       *reinterpret_cast<uint32_t*>(og + (long)qi * p.o_ld + nt * 8 + 2 * t4) = v2;
     }
     if (t4 == 0 && p.lse) p.lse[(long)bh * p.Sq + qi] = (m[r] == -INFINITY ? 0.f : m[r]) + log2f(fmaxf(l[r], 1e-30f));
@@ -243,9 +243,9 @@ __global__ void attn_bwd_pre_kernel(const AttnArgs p) {
   const int lane = threadIdx.x & 31;
   const int bh = (int)(row / p.Sq), qi = (int)(row % p.Sq);
   const int b = bh / p.H, h = bh % p.H;
-  const __nv_bfloat162 d2 = reinterpret_cast<const __nv_bfloat162*>(p.dO + b * p.dO_sb + h * p.dO_sh + (long)qi * p.dO_ld)[lane];
-  const __nv_bfloat162 o2 = reinterpret_cast<const __nv_bfloat162*>(p.o + b * p.o_sb + h * p.o_sh + (long)qi * p.o_ld)[lane];
-  float acc = __bfloat162float(d2.x) * __bfloat162float(o2.x) + __bfloat162float(d2.y) * __bfloat162float(o2.y);
+  const __half2 d2 = reinterpret_cast<const __half2*>(p.dO + b * p.dO_sb + h * p.dO_sh + (long)qi * p.dO_ld)[lane];
+  const __half2 o2 = reinterpret_cast<const __half2*>(p.o + b * p.o_sb + h * p.o_sh + (long)qi * p.o_ld)[lane];
+  float acc = __half2float(d2.x) * __half2float(o2.x) + __half2float(d2.y) * __half2float(o2.y);
   acc = warp_sum(acc);
   if (lane == 0) p.Dsum[row] = acc;
 }
@@ -258,10 +258,10 @@ __global__ void __launch_bounds__(NT) attn_bwd_dq_kernel(const AttnArgs p) {
   const int g = lane >> 2, t4 = lane & 3;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int q0 = blockIdx.x * TQ;
-  const __nv_bfloat16* qg = p.q + b * p.q_sb + h * p.q_sh;
-  const __nv_bfloat16* kg = p.k + b * p.k_sb + h * p.k_sh;
-  const __nv_bfloat16* vg = p.v + b * p.v_sb + h * p.v_sh;
-  const __nv_bfloat16* dog = p.dO + b * p.dO_sb + h * p.dO_sh;
+  const __half* qg = p.q + b * p.q_sb + h * p.q_sh;
+  const __half* kg = p.k + b * p.k_sb + h * p.k_sh;
+  const __half* vg = p.v + b * p.v_sb + h * p.v_sh;
+  const __half* dog = p.dO + b * p.dO_sb + h * p.dO_sh;
   const uint32_t sQ = smem_u32(sm), sD = sQ + 8192, sK = sQ + 2 * 8192, sV = sQ + 4 * 8192;
   int kt0, kt1;
   key_range(q0, p.Sk, p.window, kt0, kt1);
@@ -337,10 +337,10 @@ __global__ void __launch_bounds__(NT) attn_bwd_dkdv_kernel(const AttnArgs p) {
   const int g = lane >> 2, t4 = lane & 3;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const int k0 = blockIdx.x * TK;
-  const __nv_bfloat16* qg = p.q + b * p.q_sb + h * p.q_sh;
-  const __nv_bfloat16* kg = p.k + b * p.k_sb + h * p.k_sh;
-  const __nv_bfloat16* vg = p.v + b * p.v_sb + h * p.v_sh;
-  const __nv_bfloat16* dog = p.dO + b * p.dO_sb + h * p.dO_sh;
+  const __half* qg = p.q + b * p.q_sb + h * p.q_sh;
+  const __half* kg = p.k + b * p.k_sb + h * p.k_sh;
+  const __half* vg = p.v + b * p.v_sb + h * p.v_sh;
+  const __half* dog = p.dO + b * p.dO_sb + h * p.dO_sh;
   const uint32_t sK = smem_u32(sm), sV = sK + 8192, sQ = sK + 2 * 8192, sD = sK + 4 * 8192;
   // query tiles that can see this key tile
   int qt0 = 0, qt1 = (p.Sq + TQ - 1) / TQ;

@@ -12,7 +12,7 @@
 //   warp 0     TMA producer: the CTA's fixed tile once, then a ring of streamed tiles
 //   warp 1     TMEM owner and the single thread issuing tcgen05.mma
 //   warps 2-5  one thread per TMEM lane (= tile row): softmax / dS arithmetic on the f32
-//              accumulators read with tcgen05.ld; P and dS go back into TMEM as packed bf16 and
+//              accumulators read with tcgen05.ld; P and dS go back into TMEM as packed f16 and
 //              feed the next MMA directly as its A operand (A from tensor memory)
 // Tiles come in by TMA from the strided (batch, head, row) layout through 4-D tensor maps whose
 // per-batch row extent zero-fills rows past the sequence; keys past Sk and outside the band are
@@ -33,7 +33,7 @@ struct TcArgs {
   float sl2;                 // scale * log2(e)
   float scale;
   int q_tm, k_tm, v_tm, o_tm, do_tm, dq_tm;   // tensor-map coordinate order: 1 = (d, h, s, b), 0 = (d, s, h, b)
-  __nv_bfloat16* o; long o_sb, o_sh, o_ld;
+  __half* o; long o_sb, o_sh, o_ld;
   float* lse;                // forward output [B*H][Sq]
   const float* lse_in;       // backward input
   float* Dsum;               // [B*H][Sq]: written by the dq pass, read by the dk / dv pass
@@ -96,7 +96,7 @@ __device__ __forceinline__ uint64_t fadd2_rm(uint64_t a, uint64_t b) {
 // mantissa bits) and f in [0, 1), a degree-3 polynomial for 2^f fitted here by iteratively
 // reweighted least squares for minimax relative error (< 8e-5 on [0, 1)), and n added into the
 // exponent field.  x is clamped to >= -125, so arguments below give ~2^-125 instead of 0 (far
-// below what the bf16 P or the f32 row sum register).
+// below what the f16 P or the f32 row sum register).
 // which pairs of every 8 take ex2_poly2 (3 of 8: the MUFU and FMA pipes then finish together)
 __device__ constexpr bool kPolyPair[8] = {true, false, false, true, false, true, false, false};
 
@@ -140,7 +140,7 @@ __device__ __forceinline__ bool tile_visible(int r0, int nr, int k0, int nk, int
   return max(r0 + nr - 1 - k0, k0 + nk - 1 - r0) <= window;
 }
 
-// K-major [rows][64] bf16 tile (128-byte rows, 128B swizzle): descriptor of the tile, and the
+// K-major [rows][64] f16 tile (128-byte rows, 128B swizzle): descriptor of the tile, and the
 // descriptor at k-step kk (16 wide = 32 bytes further: +2 in the start-address field)
 __device__ __forceinline__ uint64_t kdesc0(uint32_t base) { return make_sdesc(base, 16, 1024); }
 __device__ __forceinline__ uint64_t kstep(uint64_t d0, int kk) { return d0 + (uint64_t)(2 * kk); }
@@ -205,7 +205,7 @@ constexpr int NSTAGE = 4;
 // ============================================================================== forward
 // CTA: two 128-query tiles of one (b, h) (warpgroup g: rows qbase + 128 g ..), key tiles of 64.
 // TMEM, per warpgroup at 256 g: S0, S1, S2 at [0, 64), [64, 128), [128, 192) (scores of three
-// key tiles in flight; P overwrites the first 32 columns of its buffer as packed bf16), O at
+// key tiles in flight; P overwrites the first 32 columns of its buffer as packed f16), O at
 // [192, 256).
 // smem: Q0 16 KB | Q1 16 KB | 4 x (K 8 KB, V 8 KB) | barriers
 constexpr int F_SMEM = 32768 + NSTAGE * 16384 + 512;
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 1) {
     {   // scores S = Q K^T of tile j for both groups into buffer j % 3, once P V (j - 3) read it
-      const uint32_t id_qk = make_idesc_bf16(128, 64, 0, 0);   // S[128 q][64 k] = Q K^T
+      const uint32_t id_qk = make_idesc_f16(128, 64, 0, 0);   // S[128 q][64 k] = Q K^T
       bool ok = waitw(q_full, 0, kErrTimeoutFull);
       for (int j = 0; j < nkt && ok; ++j) {
         const int s = j % NSTAGE;
@@ -302,14 +302,14 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const uint64_t qd = kdesc0(smem_u32(sQ + 16384 * g));
           const uint32_t tS = tbase + 256 * g + 64 * (j % 3);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS, kstep(qd, kk), kstep(kd, kk), id_qk, kk > 0 ? 1u : 0u);
           umma_commit_w(&s_full[3 * g + (j % 3)]);
         }
       }
     }
   } else if (warp == 10) {
     {   // O += P V of tile j for each group once its P is in TMEM
-      const uint32_t id_pv = make_idesc_bf16(128, 64, 0, 1);   // O[128 q][64 d] += P V (V MN-major)
+      const uint32_t id_pv = make_idesc_f16(128, 64, 0, 1);   // O[128 q][64 d] += P V (V MN-major)
       bool ok = true;
       for (int j = 0; j < nkt && ok; ++j) {
         const int s = j % NSTAGE;
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
               p1 = ex2(x1);
             }
             lsum[e & 1] = fadd2(lsum[e & 1], f2(p0, p1));
-            pk[e] = pack_bf16x2(p0, p1);
+            pk[e] = pack_f16x2(p0, p1);
           }
           tmem_st16(tS + lane_off + 16 * c, pk);
         }
@@ -434,10 +434,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint4 w4;
-            w4.x = pack_bf16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
-            w4.y = pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
-            w4.z = pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
-            w4.w = pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+            w4.x = pack_f16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+            w4.y = pack_f16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+            w4.z = pack_f16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+            w4.w = pack_f16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
             dst[c] = w4;
           }
           if (a.lse) a.lse[(long)bh * a.Sq + qi] = (m_used == -INFINITY ? 0.f : m_used) + log2f(fmaxf(l, 1e-30f));
@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 // tiles (64) of consecutive items form one stream: the TMA ring, the three score buffers and the
 // warpgroup that handles a tile (the stream index's parity) all run on across items, and the
 // next item's Q / dO load while the current item finishes.
-// TMEM: score buffers at 128 b (b < 3): S [0, 64) (dS overwrites [0, 32) as packed bf16),
+// TMEM: score buffers at 128 b (b < 3): S [0, 64) (dS overwrites [0, 32) as packed f16),
 // dP [64, 128); two dQ accumulators at 384 and 448 (alternate items).  The softmax threads also
 // form D = rowsum(dO o O) of their row (stored to Dsum for the dk / dv pass).
 // The row's O comes in with Q and dO (TMA, an item ahead), so D needs no global load at the
@@ -578,8 +578,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 1 || warp == 10) {
     {   // the whole warp walks the schedule (uniform operands); one elected lane issues
-      const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S = Q K^T, dP = dO V^T  [128 q][64 k]
-      const uint32_t id_dq = make_idesc_bf16(128, 64, 0, 1);   // dQ[128 q][64 d] += dS K (K MN-major)
+      const uint32_t id_s = make_idesc_f16(128, 64, 0, 0);    // S = Q K^T, dP = dO V^T  [128 q][64 k]
+      const uint32_t id_dq = make_idesc_f16(128, 64, 0, 1);   // dQ[128 q][64 d] += dS K (K MN-major)
       bool ok = true;
       // a cursor over the key-tile stream, resting on a tile of an item that has some (the item
       // counter ii, which picks the Q / dO / O buffer and the accumulator, counts only those)
@@ -610,9 +610,9 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const uint32_t ka = smem_u32(sKV + s * 16384), tS = tbase + 128 * (t % 3);
           const uint64_t kd = kdesc0(ka), vd = kdesc0(ka + 8192);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS + 64, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
           umma_commit_w(&s_full[t % 3]);
           ++t;
           advance(c, ii, kt);
@@ -699,11 +699,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           const int off = row * 128 + ((cc ^ (row & 7)) << 4);
           const uint4 ov = *reinterpret_cast<const uint4*>(sO + off);
           const uint4 dv = *reinterpret_cast<const uint4*>(sdO + off);
-          const __nv_bfloat162* o2 = reinterpret_cast<const __nv_bfloat162*>(&ov);
-          const __nv_bfloat162* d2 = reinterpret_cast<const __nv_bfloat162*>(&dv);
+          const __half2* o2 = reinterpret_cast<const __half2*>(&ov);
+          const __half2* d2 = reinterpret_cast<const __half2*>(&dv);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 of = __bfloat1622float2(o2[e]), df = __bfloat1622float2(d2[e]);
+            const float2 of = __half22float2(o2[e]), df = __half22float2(d2[e]);
             Dq = fmaf(of.x, df.x, Dq);
             Dq = fmaf(of.y, df.y, Dq);
           }
@@ -719,7 +719,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const int k0 = (c.t0 + j) * 64;
         const bool edge = !tile_visible(q0, 128, k0, 64, a.Sk, a.window);
         const uint64_t sc2 = f2(a.sl2, a.sl2), nl2 = f2(-lse, -lse), nd2 = f2(-Dq, -Dq);
-        // two halves of 32 keys: S / dP of a half in, its dS row (packed bf16 pairs, column e of
+        // two halves of 32 keys: S / dP of a half in, its dS row (packed f16 pairs, column e of
         // the slot holds keys 2e, 2e + 1) out to the half's 16 columns, which the other half no
         // longer reads
 #pragma unroll 1
@@ -747,7 +747,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
             }
             const uint64_t pp = f2(p0, p1);
             f2split(fmul2(pp, fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0, d1);
-            pk[e] = pack_bf16x2(d0, d1);
+            pk[e] = pack_f16x2(d0, d1);
           }
           tmem_st16(tS + lane_off + 16 * hf, pk);
         }
@@ -877,7 +877,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
     }
   } else if (warp == 1) {
     {   // S^T = K Q^T and dP^T = V dO^T of query tile i into buffer i % 3, once dV / dK (i - 3) read it
-      const uint32_t id_s = make_idesc_bf16(128, 64, 0, 0);    // S^T, dP^T [128 k][64 q]
+      const uint32_t id_s = make_idesc_f16(128, 64, 0, 0);    // S^T, dP^T [128 k][64 q]
       bool ok = waitw(kv_full, 0, kErrTimeoutFull);
       const uint64_t kd = kdesc0(smem_u32(sK)), vd = kdesc0(smem_u32(sV));
       for (int i = 0; i < nqt && ok; ++i) {
@@ -888,15 +888,15 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const uint32_t qa = smem_u32(sQd + s * 16384), tS = tbase + 128 * (i % 3);
         const uint64_t qd = kdesc0(qa), dd = kdesc0(qa + 8192);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS, kstep(kd, kk), kstep(qd, kk), id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS, kstep(kd, kk), kstep(qd, kk), id_s, kk > 0 ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) umma_bf16_w(tS + 64, kstep(vd, kk), kstep(dd, kk), id_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS + 64, kstep(vd, kk), kstep(dd, kk), id_s, kk > 0 ? 1u : 0u);
         umma_commit_w(&s_full[i % 3]);
       }
     }
   } else if (warp == 10) {
     {   // dV += P^T dO and dK += dS^T Q of query tile i once P^T / dS^T are in TMEM
-      const uint32_t id_g = make_idesc_bf16(128, 64, 0, 1);    // dV / dK [128 k][64 d] (dO / Q MN-major)
+      const uint32_t id_g = make_idesc_f16(128, 64, 0, 1);    // dV / dK [128 k][64 d] (dO / Q MN-major)
       bool ok = true;
       for (int i = 0; i < nqt && ok; ++i) {
         const int s = i % NSTAGE;
@@ -947,7 +947,7 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
       const bool edge = !tile_visible(k0, 128, q0, 64, a.Sq, a.window) || kj >= a.Sk;
       const uint64_t sc2 = f2(a.sl2, a.sl2);
       const float4* ld4 = reinterpret_cast<const float4*>(lse_b);
-      // two halves of 32 queries: S^T / dP^T of a half in, its P^T / dS^T (packed bf16) out to the
+      // two halves of 32 queries: S^T / dP^T of a half in, its P^T / dS^T (packed f16) out to the
       // first 16 columns of the half's slot (the packed halves never overlap columns still to read),
       // so about 100 values per thread are live instead of 192
 #pragma unroll 1
@@ -979,8 +979,8 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
           }
           f2split(fmul2(f2(p0, p1), fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])),
                                           f2(-dz.x, -dz.y))), d0, d1);
-          pk[e] = pack_bf16x2(p0, p1);
-          dk[e] = pack_bf16x2(d0, d1);
+          pk[e] = pack_f16x2(p0, p1);
+          dk[e] = pack_f16x2(d0, d1);
         }
         tmem_st16(tS + lane_off + 16 * hf, pk);
         tmem_st16(tS + 64 + lane_off + 16 * hf, dk);
@@ -1058,9 +1058,9 @@ int make_map4t(CUtensorMap* m, CUtensorMapDataType dt, int esize, const void* ba
   return 0;
 }
 
-int make_map4(CUtensorMap* m, const __nv_bfloat16* base, long sb, long sh, long ld, int B, int H, int S, int rows,
+int make_map4(CUtensorMap* m, const __half* base, long sb, long sh, long ld, int B, int H, int S, int rows,
               int& tm, std::string& err) {
-  return make_map4t(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, sb, sh, ld, B, H, S, 64, rows, tm, err);
+  return make_map4t(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, sb, sh, ld, B, H, S, 64, rows, tm, err);
 }
 
 TcArgs tc_args(const AttnArgs& p) {

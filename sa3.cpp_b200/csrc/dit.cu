@@ -48,18 +48,18 @@ struct DitTarget {
   float* bns = nullptr;                    // [out]
   AdapterPrep prep;
   // rows: the token rows this linear sees in a step (B (mem + T), B ctx, B T or B); ut_ld their
-  // pitch rounded up to 64.  The forward keeps u^T [16][ut_ld] bf16 in ut; the step's inputs of
-  // the grouped adapter-gradient pass (activation arena): dz [rows][out] bf16, dg [out], du^T
-  // [16][ut_ld] bf16, cb [16][out] bf16 (dora), c3 [16][16]; and the forward's input rows x_bf
+  // pitch rounded up to 64.  The forward keeps u^T [16][ut_ld] f16 in ut; the step's inputs of
+  // the grouped adapter-gradient pass (activation arena): dz [rows][out] f16, dg [out], du^T
+  // [16][ut_ld] f16, cb [16][out] f16 (dora), c3 [16][16]; and the forward's input rows x_h
   int64_t rows = 0, ut_ld = 0;
   // inert: an adapter on a weight the step never computes with (the inpaint local.* projections
   // without a local-conditioning input): carried with zero gradients, left out of every
   // per-step adapter kernel; act = the index among the other (active) targets
   bool inert = false;
   int act = -1;
-  __nv_bfloat16 *ut = nullptr, *dz = nullptr, *dut = nullptr, *cb = nullptr;
+  __half *ut = nullptr, *dz = nullptr, *dut = nullptr, *cb = nullptr;
   float *dg = nullptr, *c3 = nullptr;
-  const __nv_bfloat16* x_bf = nullptr;
+  const __half* x_h = nullptr;
   // materialized families (dora-cols, bora, every -xs form): W_eff built once per step, the
   // forward and dX GEMMs on it, the weight gradient per backward (outside the functional
   // adapters' grouped preparation and gradient passes).  offMc: the bora column magnitude;
@@ -72,16 +72,16 @@ struct DitTarget {
 
 struct DitBlockAct {
   float *x = nullptr, *rstd_a = nullptr, *rq = nullptr, *rk = nullptr, *lse_a = nullptr;
-  __nv_bfloat16* qkv = nullptr;   // qkv projection output, bf16 (read by the head preparation and its backward)
+  __half* qkv = nullptr;   // qkv projection output, f16 (read by the head preparation and its backward)
   float *yo = nullptr, *x1 = nullptr, *rstd_c = nullptr, *qf = nullptr, *rcq = nullptr, *kvf = nullptr;
   float *rck = nullptr, *lse_c = nullptr, *x2 = nullptr, *rstd_f = nullptr, *yf = nullptr;
-  __nv_bfloat16* ff = nullptr;   // ff.proj output [val | gate], bf16 (read by the SwiGLU forward and backward)
+  __half* ff = nullptr;   // ff.proj output [val | gate], f16 (read by the SwiGLU forward and backward)
   float* mod = nullptr;
-  __nv_bfloat16 *h_a = nullptr, *qkvb = nullptr, *oa = nullptr, *hc = nullptr, *cq = nullptr, *kvb = nullptr;
-  __nv_bfloat16 *oc = nullptr, *hf = nullptr, *act = nullptr;
+  __half *h_a = nullptr, *qkvb = nullptr, *oa = nullptr, *hc = nullptr, *cq = nullptr, *kvb = nullptr;
+  __half *oc = nullptr, *hf = nullptr, *act = nullptr;
   // differential attention: both softmax streams' outputs (oa = o1 - o2, oc = oc1 - oc2), the
   // second stream's log-sum-exp and the rstd of its q / k heads (null otherwise)
-  __nv_bfloat16 *o1 = nullptr, *o2 = nullptr, *oc1 = nullptr, *oc2 = nullptr;
+  __half *o1 = nullptr, *o2 = nullptr, *oc1 = nullptr, *oc2 = nullptr;
   float *lse_a2 = nullptr, *lse_c2 = nullptr, *rq2 = nullptr, *rk2 = nullptr, *rcq2 = nullptr, *rck2 = nullptr;
   float* yc = nullptr;   // cross.out output, kept when that linear has an adapter
 };
@@ -104,8 +104,8 @@ struct DitModel {
   bool mat = false;                    // a materialized family (every target is a DitTarget::mat)
   std::string adapter_type = "lora";
   float* mat_G = nullptr;              // [max out*in] f32 weight-gradient scratch (materialized)
-  __nv_bfloat16* mat_dzt = nullptr;    // [max out][mat_ldt] bf16 transposed output gradient
-  __nv_bfloat16* mat_dD = nullptr;     // [max out*in] bf16 dD of the normalisation backward
+  __half* mat_dzt = nullptr;    // [max out][mat_ldt] f16 transposed output gradient
+  __half* mat_dD = nullptr;     // [max out*in] f16 dD of the normalisation backward
   int64_t mat_ldt = 0;
   int rank = 0;
   float alpha = 1.f, s = 1.f;
@@ -132,11 +132,11 @@ struct DitModel {
   // head
   float *te_h = nullptr, *te = nullptr, *g_h = nullptr, *gsum = nullptr, *gce_h = nullptr, *gcond = nullptr;
   float *ctx_h = nullptr, *pre = nullptr, *xin0 = nullptr;
-  __nv_bfloat16 *tfeat_b = nullptr, *te_hb = nullptr, *glob_b = nullptr, *g_hb = nullptr, *gsum_b = nullptr;
-  __nv_bfloat16 *gce_hb = nullptr, *cross_b = nullptr, *ctx_hb = nullptr, *context_b = nullptr, *xt_b = nullptr;
-  __nv_bfloat16* xp_b = nullptr;
+  __half *tfeat_b = nullptr, *te_hb = nullptr, *glob_b = nullptr, *g_hb = nullptr, *gsum_b = nullptr;
+  __half *gce_hb = nullptr, *cross_b = nullptr, *ctx_hb = nullptr, *context_b = nullptr, *xt_b = nullptr;
+  __half* xp_b = nullptr;
   // tail
-  __nv_bfloat16 *xT_b = nullptr, *pout_b = nullptr;
+  __half *xT_b = nullptr, *pout_b = nullptr;
   float *pout = nullptr, *vel = nullptr, *dvel = nullptr, *loss = nullptr, *dp = nullptr, *dxT = nullptr;
   // backward temporaries
   float *gx = nullptr, *dtmp = nullptr, *dh = nullptr, *dq3 = nullptr, *Dsum = nullptr;
@@ -150,10 +150,10 @@ struct DitModel {
   float *dqf = nullptr, *dkv = nullptr, *dkvf = nullptr, *dvc2 = nullptr, *dctx = nullptr, *dmlp = nullptr;
   float *dgcond = nullptr, *dgsum = nullptr, *dxin0 = nullptr, *dxp = nullptr;
   bool need_ctx = false, need_mod = false, need_x0 = false;
-  __nv_bfloat16 *dO_b = nullptr, *dact_b = nullptr;   // dact_b: the SwiGLU output gradient, bf16
+  __half *dO_b = nullptr, *dact_b = nullptr;   // dact_b: the SwiGLU output gradient, f16
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
-  __nv_bfloat16 *dut = nullptr, *dz = nullptr, *cb = nullptr;
+  __half *dut = nullptr, *dz = nullptr, *cb = nullptr;
   int64_t ut_ld = 0;
 
   // the step recorded as a CUDA graph (SA3K_OPT_STEP_GRAPH): valid for shape (gB, gT, gC) while
@@ -211,7 +211,7 @@ static void* dmalloc(DitModel& m, size_t bytes, std::string& err) {
 // After the activation arena moved: bind every adapter to its block's input rows and u^T, refresh
 // the device descriptors (now with the gradient pointers), and build the grouped rank-16 GEMMs
 // of the DoRA preparation and of the adapter gradients.
-// The linear a weight name belongs to: its bf16 input rows in the activation arena (null for a
+// The linear a weight name belongs to: its f16 input rows in the activation arena (null for a
 // name that is not a linear of the DiT) and how many rows it sees per step.
 static int64_t target_rows(const DitModel& m, const std::string& n) {
   const int64_t B = m.B;
@@ -224,7 +224,7 @@ static int64_t target_rows(const DitModel& m, const std::string& n) {
   return B * m.T;   // pre_conv, proj_in, proj_out, post_conv
 }
 
-static const __nv_bfloat16* target_input(const DitModel& m, const std::string& n) {
+static const __half* target_input(const DitModel& m, const std::string& n) {
   if (n.compare(0, 4, "dit.") != 0) return nullptr;
   const std::string r = n.substr(4);
   if (!r.empty() && r[0] >= '0' && r[0] <= '9') {
@@ -242,7 +242,7 @@ static const __nv_bfloat16* target_input(const DitModel& m, const std::string& n
     if (k == "ff.out.weight") return a.act;
     return nullptr;
   }
-  static const struct { const char* name; __nv_bfloat16* DitModel::*x; } kHead[] = {
+  static const struct { const char* name; __half* DitModel::*x; } kHead[] = {
       {"time_embed.0.weight", &DitModel::tfeat_b}, {"time_embed.2.weight", &DitModel::te_hb},
       {"global_embed.0.weight", &DitModel::glob_b}, {"global_embed.2.weight", &DitModel::g_hb},
       {"gce.0.weight", &DitModel::gsum_b},          {"gce.2.weight", &DitModel::gce_hb},
@@ -263,8 +263,8 @@ static bool has_target(const DitModel& m, const char* fragment) {
 static int bind_adapter_grads(DitModel& m, std::string& err) {
   for (DitTarget& t : m.tg) {
     if (t.inert) continue;
-    t.x_bf = target_input(m, t.name);
-    if (!t.x_bf) {
+    t.x_h = target_input(m, t.name);
+    if (!t.x_h) {
       err = "adapter target " + t.name + " is not a linear of the DiT";
       return 1;
     }
@@ -277,7 +277,7 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
     pd.rank = p.rank; pd.dora = p.dora() ? 1 : 0; pd.s = p.s; pd.in = p.in; pd.out = p.out;
-    pd.a_bf = p.a_bf; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_bf = p.bt_bf;
+    pd.a_h = p.a_h; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_h = p.bt_h;
     pd.pt = p.pt; pd.aat = p.aat; pd.nsq = p.nsq; pd.g = p.g;
     pd.dg = t.dg; pd.dB = m.g + t.offB; pd.dA = m.g + t.offA; pd.dm = t.offM >= 0 ? m.g + t.offM : nullptr;
     pd.cb = t.cb; pd.c3 = t.c3;
@@ -292,21 +292,21 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
     grads.push_back(j);
     // dA [rank][in] += du^T x        (A = x read MN-major, stored transposed)
     j = R16Job();
-    j.a = t.x_bf; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)M;
+    j.a = t.x_h; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)M;
     j.b = t.dut; j.ldb = t.ut_ld;
     j.out = m.g + t.offA; j.ldo = t.in; j.out_trans = 1; j.atomic = 1;
     grads.push_back(j);
-    if (p.dora() && t.w->bf16) {
-      // dA += (dt2 B)^T W             (A = the bf16 base copy read MN-major, K = out)
+    if (p.dora() && t.w->f16) {
+      // dA += (dt2 B)^T W             (A = the f16 base copy read MN-major, K = out)
       j = R16Job();
-      j.a = t.w->bf16; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)t.out;
+      j.a = t.w->f16; j.lda = t.in; j.a_mn = 1; j.M = (int)t.in; j.N = p.rank; j.K = (int)t.out;
       j.b = t.cb; j.ldb = t.out;
       j.out = m.g + t.offA; j.ldo = t.in; j.out_trans = 1; j.atomic = 1;
       grads.push_back(j);
       // P^T [16][out] = (W A^T)^T
       j = R16Job();
-      j.a = t.w->bf16; j.lda = t.in; j.a_mn = 0; j.M = (int)t.out; j.N = 16; j.K = (int)t.in;
-      j.b = p.a_bf; j.ldb = t.in;
+      j.a = t.w->f16; j.lda = t.in; j.a_mn = 0; j.M = (int)t.out; j.N = 16; j.K = (int)t.in;
+      j.b = p.a_h; j.ldb = t.in;
       j.out = p.pt; j.ldo = t.out; j.out_trans = 1; j.atomic = 0;
       prep.push_back(j);
     }
@@ -316,13 +316,13 @@ static int bind_adapter_grads(DitModel& m, std::string& err) {
     err = "adapter descriptor upload failed";
     return 1;
   }
-  // every DoRA base needs its bf16 copy for the grouped P and dA terms (else the per-adapter
+  // every DoRA base needs its f16 copy for the grouped P and dA terms (else the per-adapter
   // GEMMs over the quantized codes run instead)
-  bool all_bf16 = true;
-  for (DitTarget& t : m.tg) all_bf16 = all_bf16 && (t.inert || t.mat || !t.prep.dora() || t.w->bf16);
+  bool all_f16 = true;
+  for (DitTarget& t : m.tg) all_f16 = all_f16 && (t.inert || t.mat || !t.prep.dora() || t.w->f16);
   r16_group_free(m.r16_prep);
   r16_group_free(m.r16_grads);
-  if (!all_bf16 || grads.empty()) return 0;
+  if (!all_f16 || grads.empty()) return 0;
   if (!prep.empty() && r16_group_build(m.c, prep, 24, m.r16_prep, err)) return 1;
   return r16_group_build(m.c, grads, 24, m.r16_grads, err);
 }
@@ -353,7 +353,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
       return r;
     };
     auto f = [&](int64_t n) { return static_cast<float*>(take(n * 4)); };
-    auto h = [&](int64_t n) { return static_cast<__nv_bfloat16*>(take(n * 2)); };
+    auto h = [&](int64_t n) { return static_cast<__half*>(take(n * 2)); };
     m.blk.assign(k.depth, DitBlockAct{});
     for (int l = 0; l < k.depth; ++l) {
       DitBlockAct& a = m.blk[l];
@@ -436,56 +436,56 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
 }
 
 // ------------------------------------------------------------------ linear helpers
-static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __nv_bfloat16* x,
-                   int64_t M, float* y, __nv_bfloat16* y_bf, std::string& err) {
+static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __half* x,
+                   int64_t M, float* y, __half* y_h, std::string& err) {
   if (t && t->mat) {
-    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
     GemmDesc g;   // y = x W_eff^T + bias
     g.M = (int)M; g.N = (int)t->out; g.K = (int)t->in;
     g.a = x; g.lda = t->in;
-    g.bsrc = kB_BF16_KMAJOR; g.b = t->mt.wb; g.ldb = t->in;
+    g.bsrc = kB_F16_KMAJOR; g.b = t->mt.wb; g.ldb = t->in;
     g.col_bias = bias;
     g.out = y; g.ldo = t->out;
-    g.out_bf = y_bf; g.ldo_bf = t->out;
+    g.out_h = y_h; g.ldo_h = t->out;
     g.name = "linear.fwd";
     return gemm(m.c, g, err);
   }
   LinearFwd f;
-  f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_bf = x; f.M = M; f.y = y; f.y_bf = y_bf;
+  f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_h = x; f.M = M; f.y = y; f.y_h = y_h;
   if (t) {
-    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
     f.ut = t->ut; f.ut_ld = t->ut_ld;
   }
   return linear_forward(m.c, f, err);
 }
 
 // dy == nullptr: dz_of(t) (and dg_of(t) for dora) were written by a fused producer of the gradient
-static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __nv_bfloat16* x,
-                   const float* y, const float* dy, int64_t M, float* dx, int dx_acc, __nv_bfloat16* dx_bf,
+static int lin_bwd(DitModel& m, const Weight* w, DitTarget* t, const float* bias, const __half* x,
+                   const float* y, const float* dy, int64_t M, float* dx, int dx_acc, __half* dx_h,
                    std::string& err) {
   if (t && t->mat) {
-    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
-    // dz = bf16(dy), or already written to m.dz by the fused producer of dy
-    if (dy && k_cvt_bf16(m.c, dy, M * t->out, m.dz, err)) return 1;
-    if (dx || dx_bf) {
+    if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    // dz = f16(dy), or already written to m.dz by the fused producer of dy
+    if (dy && k_cvt_f16(m.c, dy, M * t->out, m.dz, err)) return 1;
+    if (dx || dx_h) {
       GemmDesc g;   // dx = dz W_eff
       g.M = (int)M; g.N = (int)t->in; g.K = (int)t->out;
       g.a = m.dz; g.lda = t->out;
-      g.bsrc = kB_BF16_MNMAJOR; g.b = t->mt.wb; g.ldb = t->in;
+      g.bsrc = kB_F16_MNMAJOR; g.b = t->mt.wb; g.ldb = t->in;
       g.out = dx; g.ldo = t->in; g.accumulate = dx_acc;
-      g.out_bf = dx_bf; g.ldo_bf = t->in;
+      g.out_h = dx_h; g.ldo_h = t->in;
       g.name = "linear.dx";
       if (gemm(m.c, g, err)) return 1;
     }
     return mat_target_backward(m.c, t->mt, m.dz, M, x, m.mat_G, m.mat_dzt, m.mat_ldt, m.mat_dD, err);
   }
   LinearBwd b;
-  b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_bf = x; b.y = y; b.dy = dy; b.M = M;
+  b.w = w; b.ad = t ? &t->prep : nullptr; b.bias = bias; b.x_h = x; b.y = y; b.dy = dy; b.M = M;
   b.dz_ready = dy == nullptr;
-  b.dx = dx; b.dx_accumulate = dx_acc; b.dx_bf = dx_bf;
+  b.dx = dx; b.dx_accumulate = dx_acc; b.dx_h = dx_h;
   b.ut_ld = m.ut_ld;
   if (t) {
-    if (t->rows != M || t->x_bf != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
+    if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
     b.ut = t->ut; b.ut_ld = t->ut_ld;
     b.dA = m.g + t->offA; b.dB = m.g + t->offB; b.dm = t->offM >= 0 ? m.g + t->offM : nullptr;
     b.grad_accumulate = 1;
@@ -505,8 +505,8 @@ static DitTarget* target(DitModel& m, const std::string& name) {
 }
 
 // MLP of dit_head: y = W2 silu(W1 x + b1) + b2 (src/dit.h:269-274), either linear adapted
-static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_bfloat16* x, int64_t M, float* h,
-                    __nv_bfloat16* hb, float* y, __nv_bfloat16* y_bf, std::string& err) {
+static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __half* x, int64_t M, float* h,
+                    __half* hb, float* y, __half* y_h, std::string& err) {
   const Weight* w0 = m.weight(pfx + "0.weight", err);
   const Weight* w2 = m.weight(pfx + "2.weight", err);
   if (!w0 || !w2) return 1;
@@ -514,15 +514,15 @@ static int mlp_silu(DitModel& m, const std::string& pfx, bool bias, const __nv_b
   const float* b2 = bias ? m.vec(pfx + "2.bias", err) : nullptr;
   if (bias && (!b0 || !b2)) return 1;
   if (lin_fwd(m, w0, target(m, pfx + "0.weight"), b0, x, M, h, nullptr, err)) return 1;
-  if (k_silu_bf16(m.c, h, M * w0->out, hb, err)) return 1;
-  return lin_fwd(m, w2, target(m, pfx + "2.weight"), b2, hb, M, y, y_bf, err);
+  if (k_silu_f16(m.c, h, M * w0->out, hb, err)) return 1;
+  return lin_fwd(m, w2, target(m, pfx + "2.weight"), b2, hb, M, y, y_h, err);
 }
 
 // Backward of mlp_silu from dy = dL/dy [M][out]: the adapters' gradients and, with dx, dL/dx
 // (overwritten).  h = W1 x + b1 and y are the forward's; nothing runs for a frozen MLP whose
 // input gradient is not wanted.
-static int mlp_silu_bwd(DitModel& m, const std::string& pfx, bool bias, const __nv_bfloat16* x, int64_t M,
-                        const float* h, const __nv_bfloat16* hb, const float* y, const float* dy, float* dx,
+static int mlp_silu_bwd(DitModel& m, const std::string& pfx, bool bias, const __half* x, int64_t M,
+                        const float* h, const __half* hb, const float* y, const float* dy, float* dx,
                         std::string& err) {
   DitTarget *t0 = target(m, pfx + "0.weight"), *t2 = target(m, pfx + "2.weight");
   const bool inner = t0 || dx;
@@ -540,15 +540,15 @@ static int mlp_silu_bwd(DitModel& m, const std::string& pfx, bool bias, const __
 }
 
 // where the backward of linear `t` (null: a linear without adapter) expects its dz / dg
-static __nv_bfloat16* dz_of(DitModel& m, const DitTarget* t) {
+static __half* dz_of(DitModel& m, const DitTarget* t) {
   return t && !t->mat && m.r16_grads.table ? t->dz : m.dz;
 }
 static float* dg_of(DitModel& m, const DitTarget* t) { return t && !t->mat && m.r16_grads.table ? t->dg : m.dg; }
 
 // self-attention of block `a` over the prepared [q | k | v (| qd | kd)] rows: softmax stream 0
-// (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] bf16
+// (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] f16
 static AttnArgs self_attn(const DitBlockAct& a, int B, int H, int S, int D, int Q, float scale, int st,
-                          __nv_bfloat16* o) {
+                          __half* o) {
   AttnArgs r;
   r.B = B; r.H = H; r.Sq = S; r.Sk = S; r.scale = scale; r.window = -1;
   r.q = a.qkvb + (st ? 3 * D : 0); r.q_sb = (long)S * Q; r.q_sh = 64; r.q_ld = Q;
@@ -562,7 +562,7 @@ static AttnArgs self_attn(const DitBlockAct& a, int B, int H, int S, int D, int 
 // cross-attention of block `a`: queries [cq (| cqd)] [M][Dq], context rows [ck (| ckd) | cv]
 // [B C][Dk]; stream st as for self_attn
 static AttnArgs cross_attn(const DitBlockAct& a, int B, int H, int S, int C, int D, int Dq, int Dk, float scale,
-                           int st, __nv_bfloat16* o) {
+                           int st, __half* o) {
   AttnArgs r;
   r.B = B; r.H = H; r.Sq = S; r.Sk = C; r.scale = scale; r.window = -1;
   r.q = a.cq + st * D; r.q_sb = (long)S * Dq; r.q_sh = 64; r.q_ld = Dq;
@@ -584,6 +584,15 @@ static int dit_step(DitModel& m, std::string& err) {
   const bool diff = k.differential != 0;
   const int Dq = m.cq_cols(), Dk = m.ckv_cols();
 
+  // Gradient scale: the loss gradient leaves the MSE kernel multiplied by gscale, a power of two
+  // near io*T / 2, so the output gradient is (vel - target) in size and every gradient the backward
+  // stores as an f16 operand (dz, du^T, dO, the SwiGLU output gradient) sits well inside the f16
+  // normal range.  Every adapter-gradient contribution of the step is linear in the loss gradient
+  // and adds into the flat buffer, so the buffer is multiplied by gscale before the step and by
+  // 1 / gscale after it: both exact in f32, the accumulated gradients come out unscaled.
+  const float gscale = std::exp2(std::floor(std::log2(0.5f * (float)T * (float)k.io)));
+  if (m.np > 0 && k_scale(c, m.g, m.np, gscale, err)) return 1;
+
   // adapters: operand forms + DoRA norms, once per step (grouped launches over all adapters; the
   // DoRA P = W A^T GEMMs run per adapter between them)
   const int nt = m.n_active;
@@ -603,24 +612,24 @@ static int dit_step(DitModel& m, std::string& err) {
     if (t.mat && !t.inert && mat_target_build(c, t.mt, nullptr, err)) return 1;
 
   // ---------------- head (src/dit.h:286-310)
-  if (k_cvt_bf16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
+  if (k_cvt_f16(c, m.in_tfeat, (int64_t)B * k.time_dim, m.tfeat_b, err)) return 1;
   if (mlp_silu(m, "dit.time_embed.", true, m.tfeat_b, B, m.te_h, m.te_hb, m.te, nullptr, err)) return 1;
-  if (k_cvt_bf16(c, m.in_glob, (int64_t)B * k.cond_dim, m.glob_b, err)) return 1;
+  if (k_cvt_f16(c, m.in_glob, (int64_t)B * k.cond_dim, m.glob_b, err)) return 1;
   if (mlp_silu(m, "dit.global_embed.", false, m.glob_b, B, m.g_h, m.g_hb, m.g_y, nullptr, err)) return 1;
   if (k_add(c, m.g_y, m.te, (long)B * D, m.gsum, err)) return 1;
-  if (k_cvt_bf16(c, m.gsum, (int64_t)B * D, m.gsum_b, err)) return 1;
+  if (k_cvt_f16(c, m.gsum, (int64_t)B * D, m.gsum_b, err)) return 1;
   if (mlp_silu(m, "dit.gce.", true, m.gsum_b, B, m.gce_h, m.gce_hb, m.gcond, nullptr, err)) return 1;
-  if (k_cvt_bf16(c, m.in_cross, MC * k.cond_dim, m.cross_b, err)) return 1;
+  if (k_cvt_f16(c, m.in_cross, MC * k.cond_dim, m.cross_b, err)) return 1;
   if (mlp_silu(m, "dit.cond_embed.", false, m.cross_b, MC, m.ctx_h, m.ctx_hb, m.ctx_y, m.context_b, err)) return 1;
   {
     const Weight* wpre = m.weight("dit.pre_conv.weight", err);
     const Weight* win = m.weight("dit.proj_in.weight", err);
     const float* mem = m.vec("dit.memory_tokens", err);
     if (!wpre || !win || !mem) return 1;
-    if (k_cvt_bf16(c, m.in_x, MT * k.io, m.xt_b, err)) return 1;
+    if (k_cvt_f16(c, m.in_x, MT * k.io, m.xt_b, err)) return 1;
     if (lin_fwd(m, wpre, target(m, "dit.pre_conv.weight"), nullptr, m.xt_b, MT, m.pre_lin, nullptr, err)) return 1;
     if (k_add(c, m.pre_lin, m.in_x, (long)MT * k.io, m.pre, err)) return 1;
-    if (k_cvt_bf16(c, m.pre, MT * k.io, m.xp_b, err)) return 1;
+    if (k_cvt_f16(c, m.pre, MT * k.io, m.xp_b, err)) return 1;
     if (lin_fwd(m, win, target(m, "dit.proj_in.weight"), nullptr, m.xp_b, MT, m.xin0, nullptr, err)) return 1;
     float* x0 = m.blk[0].x;
     if (k_copy_rows(c, mem, 0, 0, x0, nullptr, S, 0, B, k.mem_tokens, D, err)) return 1;
@@ -678,7 +687,7 @@ static int dit_step(DitModel& m, std::string& err) {
       // differential attention (src/dit.h:152-158): o = sdpa(q, k, v) - sdpa(qd, kd, v)
       AttnArgs sd = self_attn(a, B, H, S, D, Q, scale, 1, a.o2);
       if (attn_forward(c, sd, err)) return 1;
-      if (k_sub_bf16(c, a.o1, a.o2, M * D, a.oa, err)) return 1;
+      if (k_sub_f16(c, a.o1, a.o2, M * D, a.oa, err)) return 1;
     }
     if (lin_fwd(m, wout, to, nullptr, a.oa, M, a.yo, nullptr, err)) return 1;
     // x1 = x + gate(yo), then the cross-attention branch's norm of x1
@@ -709,7 +718,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (diff) {
       AttnArgs cd = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, 1, a.oc2);
       if (attn_forward(c, cd, err)) return 1;
-      if (k_sub_bf16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
+      if (k_sub_f16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
     }
     if (lin_fwd(m, wco, tco, nullptr, a.oc, M, tco ? a.yc : m.dtmp, nullptr, err)) return 1;
     // x2 = x1 + cross-attention output, then the feed-forward branch's modulated norm of x2
@@ -741,7 +750,7 @@ static int dit_step(DitModel& m, std::string& err) {
   if (lin_fwd(m, wpo, tpo, nullptr, m.xT_b, MT, m.pout, m.pout_b, err)) return 1;
   if (lin_fwd(m, wpc, tpc, nullptr, m.pout_b, MT, m.vel_lin, nullptr, err)) return 1;
   if (k_add(c, m.vel_lin, m.pout, (long)MT * k.io, m.vel, err)) return 1;
-  if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, err)) return 1;
+  if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, gscale, err)) return 1;
 
   // ---------------- backward
   if (cudaMemcpyAsync(m.dp, m.dvel, sizeof(float) * MT * k.io, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
@@ -788,7 +797,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (m.need_mod && k_mod_grad_norm(c, m.dh, a.x2, a.rstd_f, g_ff, (int)M, D, S, ms, m.dgcond + 3 * D,
                                       m.dgcond + 4 * D, err))
       return 1;
-    // (without a cross.out adapter the norm backward also leaves gx as bf16 in m.dz: the input of
+    // (without a cross.out adapter the norm backward also leaves gx as f16 in m.dz: the input of
     // the cross.out backward; an adapted cross.out takes the f32 gradient)
     if (k_rmsnorm_mod_bwd(c, m.dh, a.x2, a.rstd_f, (int)M, D, g_ff, a.mod + 3 * D, ms, S, m.gx, tco ? nullptr : m.dz,
                           err))
@@ -819,7 +828,7 @@ static int dit_step(DitModel& m, std::string& err) {
       if (attn_backward(c, ca, kv_grad, err)) return 1;
       HeadSlice hs;
       hs.col = st * D; hs.gamma = g_cq; hs.rstd = st ? a.rcq2 : a.rcq;
-      // bf16 gradient straight into m.dz (the input of the cross.q backward), or f32 for an
+      // f16 gradient straight into m.dz (the input of the cross.q backward), or f32 for an
       // adapted cross.q
       if (k_head_prep_bwd(c, m.dtmp + st * D, Dq, a.qf, (int)M, Dq, H, hs, S, k.rot, k.rope_base, tcq ? m.dqf : nullptr,
                           tcq ? nullptr : m.dz, err, st ? -1.0f : 1.0f))
@@ -921,6 +930,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (r16_group_run(c, m.r16_grads, "lora.grads", err)) return 1;
     if (m.dora && k_dora_da_c3_all(c, m.prep_desc, nt, err)) return 1;
   }
+  if (m.np > 0 && k_scale(c, m.g, m.np, 1.0f / gscale, err)) return 1;
   return 0;
 }
 
@@ -1295,7 +1305,7 @@ int sa3k_dit_init_adapters(sa3k_dit* d, const char* adapter_type, int rank, floa
     PrepDesc pd{};
     pd.A = p.A; pd.B = p.B; pd.m = p.m; pd.bns = p.bns;
     pd.rank = p.rank; pd.dora = p.dora() ? 1 : 0; pd.s = p.s; pd.in = p.in; pd.out = p.out;
-    pd.a_bf = p.a_bf; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_bf = p.bt_bf;
+    pd.a_h = p.a_h; pd.at_x = p.at_x; pd.b_x = p.b_x; pd.bt_h = p.bt_h;
     pd.pt = p.pt; pd.aat = p.aat; pd.nsq = p.nsq; pd.g = p.g;
     descs.push_back(pd);
     m.max_out = std::max(m.max_out, p.out);

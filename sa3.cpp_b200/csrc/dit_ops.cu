@@ -52,12 +52,12 @@ __device__ __forceinline__ void ld8(const float* p, float (&v)[8]) {
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
-__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
+__device__ __forceinline__ void ld8(const __half* p, float (&v)[8]) {
   const uint4 w = *reinterpret_cast<const uint4*>(p);
   const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ww[k]));
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&ww[k]));
     v[2 * k] = f.x;
     v[2 * k + 1] = f.y;
   }
@@ -68,12 +68,12 @@ __device__ __forceinline__ void st8(float* p, const float (&v)[8]) {
   reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-__device__ __forceinline__ void st8_bf16(__nv_bfloat16* p, const float (&v)[8]) {
+__device__ __forceinline__ void st8_f16(__half* p, const float (&v)[8]) {
   uint4 o;
-  o.x = pack_bf16x2(v[0], v[1]);
-  o.y = pack_bf16x2(v[2], v[3]);
-  o.z = pack_bf16x2(v[4], v[5]);
-  o.w = pack_bf16x2(v[6], v[7]);
+  o.x = pack_f16x2(v[0], v[1]);
+  o.y = pack_f16x2(v[2], v[3]);
+  o.z = pack_f16x2(v[4], v[5]);
+  o.w = pack_f16x2(v[6], v[7]);
   *reinterpret_cast<uint4*>(p) = o;
 }
 
@@ -89,12 +89,12 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // rms_norm + adaLN modulate of one row per block, one thread per 8 columns: every load of the row
 // (x, gamma, the sample's scale / shift) is issued before the row reduction, so the whole row is
-// in flight at once.  h = bf16(x rstd gamma (1 + sc) + sh), rstd = 1 / sqrt(mean(x^2) + eps).
+// in flight at once.  h = f16(x rstd gamma (1 + sc) + sh), rstd = 1 / sqrt(mean(x^2) + eps).
 __global__ void __launch_bounds__(1024) rmsnorm_mod_fwd_kernel(const float* __restrict__ x, int T, int D,
                                                                const float* __restrict__ gamma,
                                                                const float* __restrict__ sc,
                                                                const float* __restrict__ sh, long mod_stride, int tps,
-                                                               float eps, __nv_bfloat16* __restrict__ h,
+                                                               float eps, __half* __restrict__ h,
                                                                float* __restrict__ rstd) {
   pdl_prologue();
   __shared__ float red[32];
@@ -124,13 +124,13 @@ __global__ void __launch_bounds__(1024) rmsnorm_mod_fwd_kernel(const float* __re
     v[k] *= r * gm[k];
     if (sc) v[k] = fmaf(v[k], 1.f + a[k], b[k]);
   }
-  st8_bf16(h + (long)row * D + c, v);
+  st8_f16(h + (long)row * D + c, v);
 }
 
 // The residual step of a block half fused with the norm that follows it, one row per block, one
 // thread per 8 columns: x_out = x_in + y (gate null: the cross-attention residual) or
 // x_in + y s (s = the sample's gate vector, sigmoid(1 - g) as the modulation kernel leaves it),
-// then h = bf16(rms_norm(x_out) gamma (1 + sc) + sh) and its rstd, as rmsnorm_mod_fwd.
+// then h = f16(rms_norm(x_out) gamma (1 + sc) + sh) and its rstd, as rmsnorm_mod_fwd.
 __global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __restrict__ x_in,
                                                              const float* __restrict__ y,
                                                              const float* __restrict__ gate, long gstride, int T,
@@ -138,7 +138,7 @@ __global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __rest
                                                              const float* __restrict__ gamma,
                                                              const float* __restrict__ sc,
                                                              const float* __restrict__ sh, long mod_stride, float eps,
-                                                             __nv_bfloat16* __restrict__ h, float* __restrict__ rstd) {
+                                                             __half* __restrict__ h, float* __restrict__ rstd) {
   pdl_prologue();
   __shared__ float red[32];
   const int row = blockIdx.x, c = 8 * threadIdx.x;
@@ -173,18 +173,18 @@ __global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __rest
     v[k] *= r * gm[k];
     if (sc) v[k] = fmaf(v[k], 1.f + a[k], b[k]);
   }
-  st8_bf16(h + e, v);
+  st8_f16(h + e, v);
 }
 
 // Backward of rmsnorm_mod_fwd, one row per block (as the forward): with dn = dh gamma (1 + sc),
-// gx += rstd (dn - x rstd^2 mean(dn x)); gx_bf (nullable) receives bf16(gx) as well.
+// gx += rstd (dn - x rstd^2 mean(dn x)); gx_h (nullable) receives f16(gx) as well.
 __global__ void __launch_bounds__(1024) rmsnorm_mod_bwd_kernel(const float* __restrict__ dh,
                                                                const float* __restrict__ x,
                                                                const float* __restrict__ rstd, int T, int D,
                                                                const float* __restrict__ gamma,
                                                                const float* __restrict__ sc, long mod_stride, int tps,
                                                                float* __restrict__ gx,
-                                                               __nv_bfloat16* __restrict__ gx_bf) {
+                                                               __half* __restrict__ gx_h) {
   pdl_prologue();
   __shared__ float red[32];
   const int row = blockIdx.x, c = 8 * threadIdx.x;
@@ -214,7 +214,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_mod_bwd_kernel(const float* __re
 #pragma unroll
   for (int k = 0; k < 8; ++k) g[k] += r * (d[k] - v[k] * r * dot);
   st8(gx + e, g);
-  if (gx_bf) st8_bf16(gx_bf + e, g);
+  if (gx_h) st8_f16(gx_h + e, g);
 }
 
 // RoPE of this lane's chunk j at position pos (inverse rotation when inv): first element of a pair
@@ -247,7 +247,7 @@ template <typename Y>
 __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const Y* __restrict__ y, int T, int ncols, int H,
                                                             const HeadSlices slices, int tps, float eps, int rot,
                                                             const float2* __restrict__ tab,
-                                                            __nv_bfloat16* __restrict__ out) {
+                                                            __half* __restrict__ out) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
   const int pair = blockIdx.x * 8 + warp;
@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const Y* __restrict_
       for (int k = 0; k < 8; ++k) v[k] *= r * gm[k];
     }
     if (sl.rope && (rot == 32 || rot == 64)) rope8(v, j, pos, rot, tab, false);
-    if (valid) st8_bf16(out + (long)t * ncols + col, v);
+    if (valid) st8_f16(out + (long)t * ncols + col, v);
     pos += 4;
     while (pos >= tps) pos -= tps;
   }
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
                                                             int T, int ncols, int H, HeadSlice sl, int tps, int rot,
                                                             const float2* __restrict__ tab, float gscale,
                                                             const float* g2, long g2_ld, float* dy,
-                                                            __nv_bfloat16* dy_bf) {
+                                                            __half* dy_h) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
   const int h = blockIdx.x * 8 + warp;
@@ -348,7 +348,7 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
       for (int k = 0; k < 8; ++k) gv[k] = r * (gv[k] - yv[k] * mean);
     }
     if (valid) {
-      if (dy_bf) st8_bf16(dy_bf + (long)t * ncols + sl.col + h * 64 + 8 * j, gv);
+      if (dy_h) st8_f16(dy_h + (long)t * ncols + sl.col + h * 64 + 8 * j, gv);
       else st8(dy + (long)t * ncols + sl.col + h * 64 + 8 * j, gv);
     }
     pos += 4;
@@ -358,7 +358,7 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
 
 // The self-attention head preparation's backward (q and k: inverse RoPE, then the per-head
 // rms-norm backward; v: identity) fused with the qkv projection's backward prologue: writes
-// dz = bf16(g * dy) and adds colsum(dy * y / g) into dg (DoRA; g null: dz = bf16(dy)), with
+// dz = f16(g * dy) and adds colsum(dy * y / g) into dg (DoRA; g null: dz = f16(dy)), with
 // y = the projection output qkv (no bias).  Block = 8 warps on 8 consecutive head slices of
 // [q heads | k heads | v heads (| qd heads | kd heads)] and kHpRows token rows; each lane adds
 // its 8 columns' dg sums (summed over the warp's four row groups first) once.
@@ -366,13 +366,13 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
 // stream run on +dO, so they enter negated, and the v gradient is dq3's minus dv2 (that
 // stream's dV).  Grid (ceil(nsl H / 8), ceil(T / kHpRows)).
 __global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restrict__ dq3,
-                                                            const __nv_bfloat16* __restrict__ qkv, int T, int D, int H,
+                                                            const __half* __restrict__ qkv, int T, int D, int H,
                                                             int nsl, const float* __restrict__ rq,
                                                             const float* __restrict__ rk, const float* __restrict__ rq2,
                                                             const float* __restrict__ rk2, const float* __restrict__ dv2,
                                                             const float* __restrict__ gq, const float* __restrict__ gk,
                                                             int tps, int rot, const float2* __restrict__ tab,
-                                                            const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
+                                                            const float* __restrict__ g, __half* __restrict__ dz,
                                                             float* __restrict__ dg) {
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restr
         gv[k] *= gd[k];
       }
     }
-    if (valid) st8_bf16(dz + (long)t * ncols + col, gv);
+    if (valid) st8_f16(dz + (long)t * ncols + col, gv);
     pos += 4;
     while (pos >= tps) pos -= tps;
   }
@@ -496,9 +496,9 @@ __global__ void add_kernel(const float* __restrict__ x, const float* __restrict_
 
 __device__ __forceinline__ float sigm(float x) { return 1.f / (1.f + __expf(-x)); }
 
-// out = x - y for bf16 vectors, 8 values per thread (difference taken in f32)
-__global__ void sub_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, long n8,
-                                __nv_bfloat16* __restrict__ out) {
+// out = x - y for f16 vectors, 8 values per thread (difference taken in f32)
+__global__ void sub_f16_kernel(const __half* __restrict__ x, const __half* __restrict__ y, long n8,
+                                __half* __restrict__ out) {
   pdl_prologue();
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += (long)gridDim.x * blockDim.x) {
     const uint4 a = reinterpret_cast<const uint4*>(x)[i], b = reinterpret_cast<const uint4*>(y)[i];
@@ -506,9 +506,9 @@ __global__ void sub_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&aw[k]));
-      const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[k]));
-      o[k] = pack_bf16x2(fa.x - fb.x, fa.y - fb.y);
+      const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&aw[k]));
+      const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&bw[k]));
+      o[k] = pack_f16x2(fa.x - fb.x, fa.y - fb.y);
     }
     reinterpret_cast<uint4*>(out)[i] = make_uint4(o[0], o[1], o[2], o[3]);
   }
@@ -516,33 +516,33 @@ __global__ void sub_bf16_kernel(const __nv_bfloat16* __restrict__ x, const __nv_
 
 // SwiGLU over rows: f[t] = [val (I) | gate (I)], a[t] = val * silu(gate).  Grid (I / 4 / 256
 // column blocks, T rows): each thread owns 4 consecutive columns of one row (128-bit accesses).
-// act = bf16(val * silu(gate)) of the ff.proj output f = [val | gate] (bf16 rows of 2I), eight
+// act = f16(val * silu(gate)) of the ff.proj output f = [val | gate] (f16 rows of 2I), eight
 // columns per thread (16-byte loads and stores)
-__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ f, int T, int I, __nv_bfloat16* __restrict__ a) {
+__global__ void swiglu_fwd_kernel(const __half* __restrict__ f, int T, int I, __half* __restrict__ a) {
   pdl_prologue();
   const int j = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   for (int t = blockIdx.y; t < T; t += gridDim.y) {
-    const __nv_bfloat16* fr = f + (long)t * 2 * I;
+    const __half* fr = f + (long)t * 2 * I;
     const uint4 v4 = *reinterpret_cast<const uint4*>(fr + j);
     const uint4 g4 = *reinterpret_cast<const uint4*>(fr + I + j);
     const uint32_t vw[4] = {v4.x, v4.y, v4.z, v4.w}, gw[4] = {g4.x, g4.y, g4.z, g4.w};
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vw[k]));
-      const float2 g = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[k]));
-      o[k] = pack_bf16x2(v.x * g.x * sigm(g.x), v.y * g.y * sigm(g.y));
+      const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&vw[k]));
+      const float2 g = __half22float2(*reinterpret_cast<const __half2*>(&gw[k]));
+      o[k] = pack_f16x2(v.x * g.x * sigm(g.x), v.y * g.y * sigm(g.y));
     }
     *reinterpret_cast<uint4*>(a + (long)t * I + j) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
-__global__ void silu_bf16_kernel(const float* __restrict__ x, long n, __nv_bfloat16* __restrict__ out) {
+__global__ void silu_f16_kernel(const float* __restrict__ x, long n, __half* __restrict__ out) {
   pdl_prologue();
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const float v = x[i];
-    out[i] = __float2bfloat16_rn(v * sigm(v));
+    out[i] = __float2half_rn(v * sigm(v));
   }
 }
 
@@ -609,7 +609,7 @@ __global__ void modulation_kernel(const float* __restrict__ ssg, const float* __
 }
 
 __global__ void mse_kernel(const float* __restrict__ vel, const float* __restrict__ tgt, long per, float inv,
-                           float* __restrict__ loss, float* __restrict__ dvel) {
+                           float gscale, float* __restrict__ loss, float* __restrict__ dvel) {
   pdl_prologue();
   const int b = blockIdx.y;
   float acc = 0.f;
@@ -617,7 +617,7 @@ __global__ void mse_kernel(const float* __restrict__ vel, const float* __restric
     const long e = (long)b * per + i;
     const float d = vel[e] - tgt[e];
     acc += d * d;
-    if (dvel) dvel[e] = 2.f * d * inv;
+    if (dvel) dvel[e] = 2.f * d * inv * gscale;
   }
   acc = warp_sum(acc);
   __shared__ float part[32];
@@ -630,8 +630,22 @@ __global__ void mse_kernel(const float* __restrict__ vel, const float* __restric
   }
 }
 
+__global__ void scale_kernel(float4* __restrict__ x, long n4, float s) {
+  pdl_prologue();
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    float4 v = x[i];
+    v.x *= s; v.y *= s; v.z *= s; v.w *= s;
+    x[i] = v;
+  }
+}
+
+__global__ void scale_tail_kernel(float* __restrict__ x, long from, long n, float s) {
+  pdl_prologue();
+  for (long i = from + threadIdx.x; i < n; i += blockDim.x) x[i] *= s;
+}
+
 __global__ void copy_rows_kernel(const float* __restrict__ src, int src_rows_per, int src_off, float* __restrict__ dst,
-                                 __nv_bfloat16* __restrict__ dst_bf, int dst_rows_per, int dst_off, int B, int rows,
+                                 __half* __restrict__ dst_h, int dst_rows_per, int dst_off, int B, int rows,
                                  int D) {
   pdl_prologue();
   const long n = (long)B * rows * D;
@@ -640,7 +654,7 @@ __global__ void copy_rows_kernel(const float* __restrict__ src, int src_rows_per
     const float v = src[((long)b * src_rows_per + src_off + r) * D + d];
     const long o = ((long)b * dst_rows_per + dst_off + r) * D + d;
     if (dst) dst[o] = v;
-    if (dst_bf) dst_bf[o] = __float2bfloat16_rn(v);
+    if (dst_h) dst_h[o] = __float2half_rn(v);
   }
 }
 
@@ -659,7 +673,7 @@ static int row_block(int D, std::string& err) {
 }
 
 int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, const float* sc, const float* sh,
-                      long mod_stride, int tps, float eps, __nv_bfloat16* h, float* rstd, std::string& err) {
+                      long mod_stride, int tps, float eps, __half* h, float* rstd, std::string& err) {
   const int nt = row_block(D, err);
   if (!nt) return 1;
   ProfScope prof_(c, "rmsnorm_mod_fwd");
@@ -669,7 +683,7 @@ int k_rmsnorm_mod_fwd(Ctx* c, const float* x, int T, int D, const float* gamma, 
 
 int k_residual_norm(Ctx* c, const float* x_in, const float* y, const float* gate, long gstride, int T, int D, int tps,
                     float* x_out, const float* gamma, const float* sc, const float* sh, long mod_stride, float eps,
-                    __nv_bfloat16* h, float* rstd, std::string& err) {
+                    __half* h, float* rstd, std::string& err) {
   const int nt = row_block(D, err);
   if (!nt) return 1;
   ProfScope prof_(c, "residual_norm");
@@ -679,11 +693,11 @@ int k_residual_norm(Ctx* c, const float* x_in, const float* y, const float* gate
 }
 
 int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd, int T, int D, const float* gamma,
-                      const float* sc, long mod_stride, int tps, float* gx, __nv_bfloat16* gx_bf, std::string& err) {
+                      const float* sc, long mod_stride, int tps, float* gx, __half* gx_h, std::string& err) {
   const int nt = row_block(D, err);
   if (!nt) return 1;
   ProfScope prof_(c, "rmsnorm_mod_bwd");
-  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)T, nt, 0, dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx, gx_bf);
+  launch_pdl(c, rmsnorm_mod_bwd_kernel, (unsigned)T, nt, 0, dh, x, rstd, T, D, gamma, sc, mod_stride, tps, gx, gx_h);
   return check_launch("rmsnorm_mod_bwd", err);
 }
 
@@ -713,7 +727,7 @@ static const float2* rope_table(Ctx* c, int tps, int rot, float rope_base, std::
 
 template <typename Y>
 static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
-                           float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+                           float eps, int rot, float rope_base, __half* out, std::string& err) {
   if (rot != 0 && rot != 32 && rot != 64) { err = "rope: rot must be 32 or 64"; return 1; }
   if (nslices < 1 || nslices > 5) { err = "head_prep: 1..5 slices"; return 1; }
   HeadSlices hs{};
@@ -733,18 +747,18 @@ static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const He
 }
 
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
-                    float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+                    float eps, int rot, float rope_base, __half* out, std::string& err) {
   return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err);
 }
 
-int k_head_prep_fwd(Ctx* c, const __nv_bfloat16* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
-                    int tps, float eps, int rot, float rope_base, __nv_bfloat16* out, std::string& err) {
+int k_head_prep_fwd(Ctx* c, const __half* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                    int tps, float eps, int rot, float rope_base, __half* out, std::string& err) {
   return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err);
 }
 
-int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __nv_bfloat16* qkv, int T, int D, int H, int nsl, const float* rq,
+int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __half* qkv, int T, int D, int H, int nsl, const float* rq,
                  const float* rk, const float* rq2, const float* rk2, const float* dv2, const float* gq, const float* gk,
-                 int tps, int rot, float rope_base, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
+                 int tps, int rot, float rope_base, const float* g, __half* dz, float* dg, std::string& err) {
   if (nsl != 3 && nsl != 5) { err = "qkv backward: 3 or 5 slices"; return 1; }
   const float2* tab = nullptr;
   if (rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
@@ -757,7 +771,7 @@ int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __nv_bfloat16* qkv, int T, int 
 }
 
 int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, int ncols, int H, const HeadSlice& sl,
-                    int tps, int rot, float rope_base, float* dy, __nv_bfloat16* dy_bf, std::string& err,
+                    int tps, int rot, float rope_base, float* dy, __half* dy_h, std::string& err,
                     float gscale, const float* g2, long g2_ld) {
   const float2* tab = nullptr;
   if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
@@ -765,7 +779,7 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
   launch_pdl(c, head_prep_bwd_kernel, grid, 256, 0, g, g_ld, y, T, ncols, H, sl, tps, rot, tab, gscale, g2, g2_ld, dy,
-             dy_bf);
+             dy_h);
   return check_launch("head_prep_bwd", err);
 }
 
@@ -785,11 +799,11 @@ int k_gate_bwd(Ctx* c, const float* gx, const float* gate, long gstride, int T, 
   return check_launch("gate_bwd", err);
 }
 
-int k_sub_bf16(Ctx* c, const __nv_bfloat16* x, const __nv_bfloat16* y, long n, __nv_bfloat16* out, std::string& err) {
+int k_sub_f16(Ctx* c, const __half* x, const __half* y, long n, __half* out, std::string& err) {
   if (n % 8) { err = "sub: n must be a multiple of 8"; return 1; }
-  ProfScope prof_(c, "sub_bf16");
-  launch_pdl(c, sub_bf16_kernel, gs(n / 8), 256, 0, x, y, n / 8, out);
-  return check_launch("sub_bf16", err);
+  ProfScope prof_(c, "sub_f16");
+  launch_pdl(c, sub_f16_kernel, gs(n / 8), 256, 0, x, y, n / 8, out);
+  return check_launch("sub_f16", err);
 }
 
 int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::string& err) {
@@ -798,7 +812,7 @@ int k_add(Ctx* c, const float* x, const float* y, long n, float* out, std::strin
   return check_launch("add", err);
 }
 
-int k_swiglu_fwd(Ctx* c, const __nv_bfloat16* f, int T, int I, __nv_bfloat16* a, std::string& err) {
+int k_swiglu_fwd(Ctx* c, const __half* f, int T, int I, __half* a, std::string& err) {
   ProfScope prof_(c, "swiglu_fwd");
   if (I % 8) { err = "swiglu: the hidden width must be a multiple of 8"; return 1; }
   launch_pdl(c, swiglu_fwd_kernel, dim3((unsigned)((I / 8 + 255) / 256), (unsigned)(T < 65535 ? T : 65535)), 256, 0,
@@ -806,9 +820,9 @@ int k_swiglu_fwd(Ctx* c, const __nv_bfloat16* f, int T, int I, __nv_bfloat16* a,
   return check_launch("swiglu_fwd", err);
 }
 
-int k_silu_bf16(Ctx* c, const float* x, long n, __nv_bfloat16* out, std::string& err) {
+int k_silu_f16(Ctx* c, const float* x, long n, __half* out, std::string& err) {
   ProfScope prof_(c, "silu");
-  launch_pdl(c, silu_bf16_kernel, gs(n), 256, 0, x, n, out);
+  launch_pdl(c, silu_f16_kernel, gs(n), 256, 0, x, n, out);
   return check_launch("silu", err);
 }
 
@@ -845,18 +859,31 @@ int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, flo
   return check_launch("modulation", err);
 }
 
-int k_mse(Ctx* c, const float* vel, const float* target, int B, long per, float* loss, float* dvel, std::string& err) {
+int k_mse(Ctx* c, const float* vel, const float* target, int B, long per, float* loss, float* dvel, float grad_scale,
+          std::string& err) {
   ProfScope prof_(c, "mse");
   if (cudaMemsetAsync(loss, 0, sizeof(float) * B, c->stream) != cudaSuccess) return check_launch("mse memset", err);
   dim3 grid(16, (unsigned)B);
-  launch_pdl(c, mse_kernel, grid, 256, 0, vel, target, per, 1.0f / (float)per, loss, dvel);
+  launch_pdl(c, mse_kernel, grid, 256, 0, vel, target, per, 1.0f / (float)per, grad_scale, loss, dvel);
   return check_launch("mse", err);
 }
 
-int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __nv_bfloat16* dst_bf,
+int k_scale(Ctx* c, float* x, long n, float s, std::string& err) {
+  ProfScope prof_(c, "scale");
+  if (n <= 0) return 0;
+  const long n4 = (reinterpret_cast<uintptr_t>(x) & 15) == 0 ? n / 4 : 0;
+  if (n4 > 0) {
+    const long blocks = std::min<long>((n4 + 255) / 256, (long)c->sm_count * 8);
+    launch_pdl(c, scale_kernel, (unsigned)blocks, 256, 0, reinterpret_cast<float4*>(x), n4, s);
+  }
+  if (4 * n4 < n) launch_pdl(c, scale_tail_kernel, 1, 256, 0, x, 4 * n4, n, s);
+  return check_launch("scale", err);
+}
+
+int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __half* dst_h,
                 int dst_rows_per, int dst_off, int B, int rows, int D, std::string& err) {
   ProfScope prof_(c, "copy_rows");
-  launch_pdl(c, copy_rows_kernel, gs((long)B * rows * D), 256, 0, src, src_rows_per, src_off, dst, dst_bf, dst_rows_per,
+  launch_pdl(c, copy_rows_kernel, gs((long)B * rows * D), 256, 0, src, src_rows_per, src_off, dst, dst_h, dst_rows_per,
                                                                   dst_off, B, rows, D);
   return check_launch("copy_rows", err);
 }

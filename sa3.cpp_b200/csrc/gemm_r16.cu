@@ -6,11 +6,11 @@
 // dA += (dt2 B)^T W, src/train_lora.h's functional LoRA / DoRA backward as derived by
 // ggml_build_backward_expand, src/train_ckpt.h:400) and the DoRA P = W A^T of the forward are all
 // such "skinny" contractions over a long K: they only stream their A operand (an activation,
-// an output gradient or the bf16 base copy) once.  Run one at a time they are latency-bound
+// an output gradient or the f16 base copy) once.  Run one at a time they are latency-bound
 // launches of a few dozen CTAs; grouped, every SM streams A tiles at HBM speed.
 //
 // Work items are (problem, 128-row M tile, K range); persistent CTAs walk the global item list.
-// Each CTA: warp 0 TMA producer (A tile 128 x 64 bf16, K-major or MN-major, and the 16 x 64 B
+// Each CTA: warp 0 TMA producer (A tile 128 x 64 f16, K-major or MN-major, and the 16 x 64 B
 // tile), warp 1 TMEM owner + MMA issue (tcgen05.mma kind::f16, M = 128, N = 16, one elected
 // lane), warps 2-5 epilogue (tcgen05.ld of the 128 x 16 f32 accumulator, alpha, f32 atomic add
 // or plain store).  The accumulator is double-buffered in TMEM (2 x 16 columns).
@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t aoff0 = smem_u32(smem + kOffA), boff0 = smem_u32(smem + kOffB);
     const uint64_t bdesc0 = make_sdesc(boff0, 16, 1024);
     const uint64_t adesc_k = make_sdesc(aoff0, 16, 1024), adesc_mn = make_sdesc(aoff0, 8192, 1024);
-    const uint32_t idesc_k = make_idesc_bf16(128, 16, 0, 0), idesc_mn = make_idesc_bf16(128, 16, 1, 0);
+    const uint32_t idesc_k = make_idesc_f16(128, 16, 0, 0), idesc_mn = make_idesc_f16(128, 16, 1, 0);
     int it = 0, ti = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < nitems && ok; item += gridDim.x, ++ti) {
@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t aoff = (uint32_t)(s * kA) >> 4, boff = (uint32_t)(s * kB) >> 4;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_bf16_w(d_tmem, adesc0 + aoff + kk * akstep, bdesc0 + boff + kk * 2u, idesc,
+          umma_f16_w(d_tmem, adesc0 + aoff + kk * akstep, bdesc0 + boff + kk * 2u, idesc,
                       (kb > 0 || kk > 0) ? 1u : 0u);
         umma_commit_w(&empty[s]);
       }
@@ -248,7 +248,7 @@ static int map2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t oute
   cuuint64_t strides[1] = {row_bytes};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
-  if (enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+  if (enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
     err = std::string(what) + ": cuTensorMapEncodeTiled failed";

@@ -8,17 +8,17 @@
 namespace sa3k {
 
 // out (+)= alpha * Aop * Bop for one problem of a group:
-//   Aop [M x K] bf16: K-major A[m * lda + k] (a_mn 0) or MN-major A[k * lda + m] (a_mn 1)
-//   Bop [K x N] bf16, N <= 16, stored K-major as B[n * ldb + k] (rows n >= N are never used
+//   Aop [M x K] f16: K-major A[m * lda + k] (a_mn 0) or MN-major A[k * lda + m] (a_mn 1)
+//   Bop [K x N] f16, N <= 16, stored K-major as B[n * ldb + k] (rows n >= N are never used
 //       in the output, but the 16 x 64 tile is loaded: ldb rows 0..15 must be readable)
 //   out f32: out[m * ldo + n] or (out_trans) out[n * ldo + m]; atomic: added with f32 atomics
 //       (K may then be split across CTAs), else stored once (no split).
 struct R16Job {
-  const __nv_bfloat16* a = nullptr;
+  const __half* a = nullptr;
   long lda = 0;
   int a_mn = 0;
   int M = 0, N = 16, K = 0;
-  const __nv_bfloat16* b = nullptr;
+  const __half* b = nullptr;
   long ldb = 0;
   float alpha = 1.0f;
   float* out = nullptr;

@@ -83,14 +83,14 @@ static int* split_counters(Ctx* c, std::string& err) {
 // Tail split: when the tiles leave a last, partial round on `slots` CTAs (or CTA pairs), split
 // each of those tiles' K range into parts spread over every slot; the parts add into the output,
 // which is zeroed first over the column band of the tail tiles unless the GEMM accumulates.
-// f32 output only (bf16 partial sums cannot be added), no split-K.
+// f32 output only (f16 partial sums cannot be added), no split-K.
 static int plan_tail(Ctx* c, const GemmDesc& d, GemmArgs& a, long tiles, long slots, int tiles_m, int bn,
                      std::string& err) {
   const int nkb = (d.K + kBK - 1) / kBK;
   a.tail_t0 = (int)tiles;
   a.tail_parts = 1;
   a.tail_kbps = nkb;
-  if (a.splits != 1 || !d.out || d.out_bf || d.out_bf_t || tiles <= slots) return 0;
+  if (a.splits != 1 || !d.out || d.out_h || d.out_h_t || tiles <= slots) return 0;
   const long rem = tiles % slots;
   if (rem == 0) return 0;
   int parts = (int)(slots / rem);
@@ -132,7 +132,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   a.partial = nullptr;
   // (splits that end in the in-kernel reduction keep >= 16 k-blocks each: below that the
   // reduction by the last CTA of a tile costs more than the shorter K loop saves)
-  const int min_kb = (d.atomic_split && d.out && !d.out_bf) ? 4 : 16;
+  const int min_kb = (d.atomic_split && d.out && !d.out_h) ? 4 : 16;
   if (tiles * 2 <= (long)c->sm_count && nkb >= 2 * min_kb) {
     int splits = (int)((long)c->sm_count / tiles);
     if (splits > nkb / min_kb) splits = nkb / min_kb;
@@ -141,7 +141,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
       splits = (nkb + kps - 1) / kps;
       a.splits = splits;
       a.kb_per_split = kps;
-      if (d.atomic_split && d.out && !d.out_bf) {
+      if (d.atomic_split && d.out && !d.out_h) {
         // the splits add into `out` directly; without accumulation it starts from zero
         a.atomic = 1;
         if (!d.accumulate) {
@@ -165,13 +165,13 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   a.tma_out = 0;
   if (a.splits == 1) {
     std::string e2;
-    if (d.out && !d.out_bf && !d.out_bf_t && !d.out_trans && (d.ldo % 4) == 0 &&
+    if (d.out && !d.out_h && !d.out_h_t && !d.out_trans && (d.ldo % 4) == 0 &&
         (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
         !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d.out, d.N, d.M, d.ldo * 4, 32, 32, SW, "out", e2))
       a.tma_out = 1;
-    else if (d.out_bf && !d.out && !d.out_bf_trans && !d.out_bf_t && d.bf_scale == 1.0f && BN >= 64 && (d.ldo_bf % 8) == 0 &&
-             (reinterpret_cast<uintptr_t>(d.out_bf) & 15) == 0 &&
-             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
+    else if (d.out_h && !d.out && !d.out_h_trans && !d.out_h_t && d.h_scale == 1.0f && BN >= 64 && (d.ldo_h % 8) == 0 &&
+             (reinterpret_cast<uintptr_t>(d.out_h) & 15) == 0 &&
+             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, d.out_h, d.N, d.M, d.ldo_h * 2, 64, 32, SW, "out_h", e2))
       a.tma_out = 2;
   }
   const long items = a.tail_parts > 1 ? a.tail_t0 + (tiles - a.tail_t0) * a.tail_parts : tiles * a.splits;
@@ -184,7 +184,7 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   return 0;
 }
 
-// CTA-pair launch (cta_group::2, clusters of 2): bf16 operands, no split-K.
+// CTA-pair launch (cta_group::2, clusters of 2): f16 operands, no split-K.
 template <int BN, int STAGES, int BMODE>
 static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtensorMap& tb,
                        const CUtensorMap& tea, const CUtensorMap& teb, const GemmArgs& args, std::string& err) {
@@ -219,12 +219,12 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
   a.tma_out = 0;
   {
     std::string e2;
-    if (d.out && !d.out_bf && !d.out_trans && (d.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
+    if (d.out && !d.out_h && !d.out_trans && (d.ldo % 4) == 0 && (reinterpret_cast<uintptr_t>(d.out) & 15) == 0 &&
         !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, d.out, d.N, d.M, d.ldo * 4, 32, 32, SW, "out", e2))
       a.tma_out = 1;
-    else if (d.out_bf && !d.out && !d.out_bf_trans && (d.ldo_bf % 8) == 0 &&
-             (reinterpret_cast<uintptr_t>(d.out_bf) & 15) == 0 &&
-             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, d.out_bf, d.N, d.M, d.ldo_bf * 2, 64, 32, SW, "out_bf", e2))
+    else if (d.out_h && !d.out && !d.out_h_trans && (d.ldo_h % 8) == 0 &&
+             (reinterpret_cast<uintptr_t>(d.out_h) & 15) == 0 &&
+             !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, d.out_h, d.N, d.M, d.ldo_h * 2, 64, 32, SW, "out_h", e2))
       a.tma_out = 2;
   }
   const long tiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + BN - 1) / BN);
@@ -273,10 +273,10 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
     return 1;
   }
   const bool weight_b = d.bsrc == kB_WEIGHT_NT || d.bsrc == kB_WEIGHT_TN;
-  // quantized weights run through the in-smem dequant path unless a bf16 operand copy exists
+  // quantized weights run through the in-smem dequant path unless a f16 operand copy exists
   // and the context has not asked for the in-smem path explicitly
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
-                     !(d.w->bf16 && !c->smem_dequant);
+                     !(d.w->f16 && !c->smem_dequant);
   int bn = d.bn;
   if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N, quant);
   if (quant && bn == 192) bn = 256;
@@ -288,7 +288,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   memset(&tbs, 0, sizeof tbs);
   memset(&tea, 0, sizeof tea);
   memset(&teb, 0, sizeof teb);
-  const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto BF = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
   const auto NOSW = CU_TENSOR_MAP_SWIZZLE_NONE;
 
@@ -298,10 +298,10 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
     if (make_map(&ta, BF, d.a, d.K, d.M, d.lda * 2, 64, kBM, SW, "A", err)) return 1;
   }
   int bmode = 0;
-  if (d.bsrc == kB_BF16_KMAJOR) {
+  if (d.bsrc == kB_F16_KMAJOR) {
     bmode = 0;
     if (make_map(&tb, BF, d.b, d.K, d.N, d.ldb * 2, 64, bn, SW, "B", err)) return 1;
-  } else if (d.bsrc == kB_BF16_MNMAJOR) {
+  } else if (d.bsrc == kB_F16_MNMAJOR) {
     bmode = 1;
     if (make_map(&tb, BF, d.b, d.N, d.K, d.ldb * 2, 64, 64, SW, "B (MN-major)", err)) return 1;
   } else {
@@ -334,13 +334,13 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
         if (make_map(&tbs, U64, w->scales, w->out, w->in / 32, w->out * 8, 64, bn / 32, NOSW, "Q4_K scales", err)) return 1;
       }
     } else {
-      // F16 / F32 bases, and quantized bases with a dequantized cache, run on the bf16 copy
+      // F16 / F32 bases, and quantized bases with a dequantized cache, run on the f16 copy
       if (nt) {
         bmode = 0;
-        if (make_map(&tb, BF, w->bf16, w->in, w->out, w->in * 2, 64, bn, SW, "W bf16", err)) return 1;
+        if (make_map(&tb, BF, w->f16, w->in, w->out, w->in * 2, 64, bn, SW, "W f16", err)) return 1;
       } else {
         bmode = 1;
-        if (make_map(&tb, BF, w->bf16, w->in, w->out, w->in * 2, 64, 64, SW, "W^T bf16", err)) return 1;
+        if (make_map(&tb, BF, w->f16, w->in, w->out, w->in * 2, 64, 64, SW, "W^T f16", err)) return 1;
       }
     }
   }
@@ -359,8 +359,8 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.has_ext = d.ext_at ? 1 : 0;
   a.col_scale = d.col_scale; a.col_bias = d.col_bias; a.alpha = d.alpha;
   a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
-  a.out_bf = d.out_bf; a.ldo_bf = d.ldo_bf; a.out_bf_trans = d.out_bf_trans; a.bf_scale = d.bf_scale;
-  a.out_bf_t = d.out_bf_t; a.ldo_bf_t = d.ldo_bf_t;
+  a.out_h = d.out_h; a.ldo_h = d.ldo_h; a.out_h_trans = d.out_h_trans; a.h_scale = d.h_scale;
+  a.out_h_t = d.out_h_t; a.ldo_h_t = d.ldo_h_t;
   a.tile_cnt = nullptr;
   a.tail_t0 = 0;
   a.tail_parts = 1;
@@ -373,17 +373,17 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.atomic = 0;
 
   if (bn == 16) {
-    if (bmode != 0) { err = "gemm: N tile 16 supports bf16 K-major B only"; return 1; }
+    if (bmode != 0) { err = "gemm: N tile 16 supports f16 K-major B only"; return 1; }
     return d.a_mn ? launch<16, 8, 0, true>(c, d, ta, tb, tbs, tea, teb, a, err)
                   : launch<16, 8, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);
   }
   if (d.a_mn) { err = "gemm: MN-major A is only instantiated with the 16-wide N tile"; return 1; }
-  // CTA pairs for the bf16-operand GEMMs with at least one full round of pair tiles (measured on
+  // CTA pairs for the f16-operand GEMMs with at least one full round of pair tiles (measured on
   // the DiT shapes: pairs match or beat the one-CTA kernel from there on; half the B bytes per
   // SM per MMA cycle).  The pair N tile (256, or 192 for K-major B) minimises rounds x tile
   // width / efficiency, 256 x 192 pair tiles running at about 0.85 of 256 x 256 per column.
   // gemm_pair 2 forces pairs wherever they apply (tile_n 192 picks 256 x 192 pair tiles).
-  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM && d.N >= 256 && !d.out_bf_t && d.bf_scale == 1.0f) {
+  if (c->gemm_pair && bmode < 2 && d.M >= 2 * kBM && d.N >= 256 && !d.out_h_t && d.h_scale == 1.0f) {
     int bp = 0;
     if (c->gemm_pair == 2) {
       bp = (c->tile_n == 192 && bmode == 0) ? 192 : 256;
@@ -401,9 +401,9 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       CUtensorMap tb2 = tb, tea2 = tea, teb2 = teb;
       // B halves: BN/2 rows (K-major) per CTA; MN-major B keeps its 64-wide atoms
       if (bmode == 0) {
-        const void* bptr = d.bsrc == kB_BF16_KMAJOR ? d.b : d.w->bf16;
-        const long bk = d.bsrc == kB_BF16_KMAJOR ? d.K : d.w->in;
-        const long bld = d.bsrc == kB_BF16_KMAJOR ? d.ldb * 2 : d.w->in * 2;
+        const void* bptr = d.bsrc == kB_F16_KMAJOR ? d.b : d.w->f16;
+        const long bk = d.bsrc == kB_F16_KMAJOR ? d.K : d.w->in;
+        const long bld = d.bsrc == kB_F16_KMAJOR ? d.ldb * 2 : d.w->in * 2;
         if (make_map(&tb2, BF, bptr, bk, d.N, bld, 64, bp / 2, SW, "B half", err)) return 1;
       }
       if (d.ext_at) {

@@ -6,27 +6,27 @@
 // their backward (ggml_build_backward_expand at src/train_ckpt.h:400).  One CTA computes one
 // 128 x BN output tile with a warp-specialized pipeline:
 //
-//   warp 0      TMA producer: A tile (bf16) + B tile (bf16) or the raw quantized B bytes + scales
+//   warp 0      TMA producer: A tile (f16) + B tile (f16) or the raw quantized B bytes + scales
 //   warp 1      TMEM allocator and MMA issue (tcgen05.mma kind::f16, one elected lane)
-//   warps 2-5   dequant stage (quantized B only): raw bytes -> bf16 in the 128B-swizzled UMMA
+//   warps 2-5   dequant stage (quantized B only): raw bytes -> f16 in the 128B-swizzled UMMA
 //               layout, then the epilogue: tcgen05.ld of the accumulator -> scale/bias -> global
 //
-// Operand layouts in shared memory (bf16, 128-byte swizzle, BK = 64 = one swizzle row):
+// Operand layouts in shared memory (f16, 128-byte swizzle, BK = 64 = one swizzle row):
 //   K-major:  [rows][64] -- row r at r*128 B, 8-row groups of 1024 B (SBO = 1024);
 //             advancing K by 16 moves the start address by 32 B.
 //   MN-major: [64 k-rows][64 mn] atoms of 8 KB, atom j (mn 64j..) at j*8192 (LBO = 8192),
 //             8-k-row groups at 1024 B (SBO = 1024); advancing K by 16 moves by 2048 B.
 //
 // B operand modes (BMODE):
-//   0  bf16 K-major via TMA  ([N][K] row-major in HBM)
-//   1  bf16 MN-major via TMA ([K][N] row-major in HBM)
+//   0  f16 K-major via TMA  ([N][K] row-major in HBM)
+//   1  f16 MN-major via TMA ([K][N] row-major in HBM)
 //   2  Q8_0 "NT": W[out = N][in = K] quantized along K, dequantized K-major      (forward)
 //   3  Q8_0 "TN": W[out = K][in = N] quantized along N, dequantized MN-major     (dX = W^T dy)
 //   4  Q4_K "NT", 5  Q4_K "TN": as 2 / 3 with 4-bit codes.
 // Quantized weights live in HBM repacked by quant.cu: int8 codes (Q8_0) or natural-order nibble
 // pairs (Q4_K) as [out][in], and per-32-element scales as [in/32][out] f32 (Q8_0: d) or
 // float2 (Q4_K: d*sc, dmin*m) -- the same numbers the GGUF blocks encode, so the dequantized
-// values are bit-identical to ggml's to_float (then rounded once to bf16 for the tensor core).
+// values are bit-identical to ggml's to_float (then rounded once to f16 for the tensor core).
 #pragma once
 
 #include "sa3k_common.cuh"
@@ -43,12 +43,12 @@ struct GemmArgs {
   long ldo;                 // its leading dimension (elements)
   int out_trans;            // 0: out[m*ldo + n]; 1: out[n*ldo + m]
   int accumulate;           // add into out instead of overwriting
-  __nv_bfloat16* out_bf;    // bf16 output (nullable): bf_scale * the value written to out
-  long ldo_bf;
-  int out_bf_trans;
-  float bf_scale;
-  __nv_bfloat16* out_bf_t;  // second bf16 output, transposed: out_bf_t[n * ldo_bf_t + m] (nullable)
-  long ldo_bf_t;
+  __half* out_h;    // f16 output (nullable): h_scale * the value written to out
+  long ldo_h;
+  int out_h_trans;
+  float h_scale;
+  __half* out_h_t;  // second f16 output, transposed: out_h_t[n * ldo_h_t + m] (nullable)
+  long ldo_h_t;
   int splits;               // split-K: work item = (tile, split); 1 = no split
   int kb_per_split;         // 64-wide k-blocks per split
   float* partial;           // split-K: raw f32 partial sums [splits][M][N]; the CTA that finishes a
@@ -57,7 +57,7 @@ struct GemmArgs {
   int tail_t0;              // tail split: tiles [tail_t0, ntiles) (the last, partial round) run as
   int tail_parts;           //   tail_parts K ranges of tail_kbps k-blocks each, added into the
   int tail_kbps;            //   output (pre-zeroed unless accumulating); tail_parts <= 1: off
-  int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: bf16 `out_bf` via TMA
+  int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: f16 `out_h` via TMA
                             //    store; 0: direct stores (split-K partials, transposed or dual outputs)
   int atomic;               // split-K: every split adds its (scaled) part into `out` with atomics
   int* err;                 // device error word
@@ -117,7 +117,7 @@ struct BModeTraits {
 
 __host__ __device__ constexpr int align_up(int x, int a) { return (x + a - 1) / a * a; }
 
-// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, then the epilogue warps (8 for bf16
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, then the epilogue warps (8 for f16
 // operands: two per TMEM lane quarter, splitting the accumulator columns; 4 with the dequant
 // stage), then the dequant warps (quantized B only).
 template <int BMODE>
@@ -163,7 +163,7 @@ struct GemmSmem {
 };
 
 // ------------------------------------------------------------------ dequantization stages
-// NT threads of the dequant warps each write BN*8/NT 16-byte chunks (8 bf16) of the B stage.
+// NT threads of the dequant warps each write BN*8/NT 16-byte chunks (8 f16) of the B stage.
 
 // Codes to f32 without the int-to-float conversion unit (a quarter-rate pipe): a byte c placed in
 // the low mantissa byte of 2^23 (bits 0x4B0000cc, one byte permute) is the float 2^23 + c
@@ -185,7 +185,7 @@ __device__ __forceinline__ uint4 q8_chunk(uint2 q, float s) {
     const int b = 2 * (k & 1);
     float lo, hi;
     f2split(fmul2(fadd2(f2(magic_code(ww, b), magic_code(ww, b + 1)), bias), sc), lo, hi);
-    o[k] = pack_bf16x2(lo, hi);
+    o[k] = pack_f16x2(lo, hi);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -201,7 +201,7 @@ __device__ __forceinline__ uint4 q4_chunk(uint32_t nib, float d, float m) {
   for (int b = 0; b < 4; ++b) {   // elements 2b (low nibble) and 2b + 1 (high nibble)
     float v0, v1;
     f2split(ffma2(dd, fadd2(f2(magic_code(lo4, b), magic_code(hi4, b)), bias), mm), v0, v1);
-    o[b] = pack_bf16x2(v0, v1);
+    o[b] = pack_f16x2(v0, v1);
   }
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
@@ -290,7 +290,7 @@ __device__ __forceinline__ void epi_columns(const uint32_t (&v)[32], float* f, i
 __device__ __forceinline__ void splitk_finish(const GemmArgs& args, int m0, int n0, int rows, int cols, int tid,
                                               int nt) {
   const long mn = (long)args.M * args.N;
-  const bool trans = args.out_trans || args.out_bf_trans || args.out_bf_t;
+  const bool trans = args.out_trans || args.out_h_trans || args.out_h_t;
   const int vw = (args.N % 4 == 0) ? 4 : 1;
   const int cg = (cols + vw - 1) / vw;
   for (int e = tid; e < rows * cg; e += nt) {
@@ -319,12 +319,12 @@ __device__ __forceinline__ void splitk_finish(const GemmArgs& args, int m0, int 
         float* dst = args.out_trans ? args.out + (long)col * args.ldo + row : args.out + (long)row * args.ldo + col;
         *dst = args.accumulate ? *dst + v : v;
       }
-      if (args.out_bf) {
-        __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)col * args.ldo_bf + row
-                                               : args.out_bf + (long)row * args.ldo_bf + col;
-        *dst = __float2bfloat16_rn(v * args.bf_scale);
+      if (args.out_h) {
+        __half* dst = args.out_h_trans ? args.out_h + (long)col * args.ldo_h + row
+                                               : args.out_h + (long)row * args.ldo_h + col;
+        *dst = __float2half_rn(v * args.h_scale);
       }
-      if (args.out_bf_t) args.out_bf_t[(long)col * args.ldo_bf_t + row] = __float2bfloat16_rn(v);
+      if (args.out_h_t) args.out_h_t[(long)col * args.ldo_h_t + row] = __float2half_rn(v);
     }
   }
 }
@@ -359,12 +359,12 @@ __device__ __forceinline__ void splitk_finish_rows16(const GemmArgs& args, int m
       float* dst = args.out_trans ? args.out + (long)col * args.ldo + row : args.out + (long)row * args.ldo + col;
       *dst = args.accumulate ? *dst + v : v;
     }
-    if (args.out_bf) {
-      __nv_bfloat16* dst = args.out_bf_trans ? args.out_bf + (long)col * args.ldo_bf + row
-                                             : args.out_bf + (long)row * args.ldo_bf + col;
-      *dst = __float2bfloat16_rn(v * args.bf_scale);
+    if (args.out_h) {
+      __half* dst = args.out_h_trans ? args.out_h + (long)col * args.ldo_h + row
+                                             : args.out_h + (long)row * args.ldo_h + col;
+      *dst = __float2half_rn(v * args.h_scale);
     }
-    if (args.out_bf_t) args.out_bf_t[(long)col * args.ldo_bf_t + row] = __float2bfloat16_rn(v);
+    if (args.out_h_t) args.out_h_t[(long)col * args.ldo_h_t + row] = __float2half_rn(v);
   }
 }
 
@@ -511,8 +511,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
     // address >> 4) is advanced by adding the byte offset >> 4 (shared addresses stay below
     // 2^18, so the field never carries into the next one).
     const WaiterW<> wt{abort_flag, args.err};
-    const uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
-    const uint32_t idesc_ext = make_idesc_bf16(kBM, BN, 1, 0);   // A = u^T read MN-major
+    const uint32_t idesc = make_idesc_f16(kBM, BN, A_MN ? 1 : 0, T::mn ? 1 : 0);
+    const uint32_t idesc_ext = make_idesc_f16(kBM, BN, 1, 0);   // A = u^T read MN-major
     const uint64_t adesc0 = A_MN ? make_sdesc(smem_u32(smem + L::OFF_A), 8192, 1024)
                                  : make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
     const uint64_t bdesc0 = T::mn ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
@@ -541,10 +541,10 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         if (kb < nkb) {
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_bf16_w(d_tmem, adesc0 + aoff + kk * A_KSTEP, bdesc0 + boff + kk * B_KSTEP, idesc,
+            umma_f16_w(d_tmem, adesc0 + aoff + kk * A_KSTEP, bdesc0 + boff + kk * B_KSTEP, idesc,
                         (kb > 0 || kk > 0) ? 1u : 0u);
         } else {
-          umma_bf16_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
+          umma_f16_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
         }
         umma_commit_w(&empty[s]);
       }
@@ -553,7 +553,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
   } else if (warp < 2 + R::EPI_WARPS) {
     // ------------------------------------------------------------ epilogue
     // Each warp drains 32 TMEM lanes (32 output rows); with 8 epilogue warps the two warps of a
-    // lane quarter take alternate column chunks.  TMA path (args.tma_out): 32 f32 (or 64 bf16)
+    // lane quarter take alternate column chunks.  TMA path (args.tma_out): 32 f32 (or 64 f16)
     // columns per step are written into a 128B-swizzled 32-row staging buffer and sent with one
     // asynchronous TMA store (reduce-add when accumulating); two buffers alternate when they fit.
     // Direct path: the same staging buffer transposes each 32 x 32 block so every global store
@@ -618,10 +618,10 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               uint4 o;
-              o.x = pack_bf16x2(f[8 * c], f[8 * c + 1]);
-              o.y = pack_bf16x2(f[8 * c + 2], f[8 * c + 3]);
-              o.z = pack_bf16x2(f[8 * c + 4], f[8 * c + 5]);
-              o.w = pack_bf16x2(f[8 * c + 6], f[8 * c + 7]);
+              o.x = pack_f16x2(f[8 * c], f[8 * c + 1]);
+              o.y = pack_f16x2(f[8 * c + 2], f[8 * c + 3]);
+              o.z = pack_f16x2(f[8 * c + 4], f[8 * c + 5]);
+              o.w = pack_f16x2(f[8 * c + 6], f[8 * c + 7]);
               *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = o;
             }
           }
@@ -647,9 +647,9 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
               if (add) atomicAdd(dst, f[j]);
               else *dst = args.accumulate ? *dst + f[j] : f[j];
             }
-            if (args.out_bf && args.out_bf_trans)
-              args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j] * args.bf_scale);
-            if (args.out_bf_t) args.out_bf_t[(long)(nb + j) * args.ldo_bf_t + myrow] = __float2bfloat16_rn(f[j]);
+            if (args.out_h && args.out_h_trans)
+              args.out_h[(long)(nb + j) * args.ldo_h + myrow] = __float2half_rn(f[j] * args.h_scale);
+            if (args.out_h_t) args.out_h_t[(long)(nb + j) * args.ldo_h_t + myrow] = __float2half_rn(f[j]);
           }
         }
         if (BN == 16 && split_out && args.N == 16) {
@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
           }
           continue;
         }
-        if (split_out || (args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
+        if (split_out || (args.out && !args.out_trans) || (args.out_h && !args.out_h_trans)) {
           float* st32 = reinterpret_cast<float*>(stg);     // 32 x 32 f32, XOR-swizzled columns
 #pragma unroll
           for (int j = 0; j < 32; ++j) st32[lane * 32 + (j ^ lane)] = f[j];
@@ -681,8 +681,8 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
               if (add) atomicAdd(dst, x);
               else *dst = args.accumulate ? *dst + x : x;
             }
-            if (args.out_bf && !args.out_bf_trans)
-              args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x * args.bf_scale);
+            if (args.out_h && !args.out_h_trans)
+              args.out_h[(long)row * args.ldo_h + nb + lane] = __float2half_rn(x * args.h_scale);
           }
           __syncwarp();
         }
@@ -725,7 +725,7 @@ __global__ void __launch_bounds__(GemmRoles<BMODE>::THREADS, 1)
         const int nkb = w.nkb, total = w.total;
         for (int kb = 0; kb < total; ++kb, ++it) {
           // Every stage use is observed (and acknowledged on bready), the extension stage too
-          // (it is loaded as bf16 by TMA and needs no work): skipping a phase would make the
+          // (it is loaded as f16 by TMA and needs no work): skipping a phase would make the
           // next parity wait on this barrier alias with an older phase.
           const int s = it % STAGES;
           const uint32_t use = (uint32_t)(it / STAGES);

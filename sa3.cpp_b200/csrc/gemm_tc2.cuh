@@ -1,4 +1,4 @@
-// gemm_tc2.cuh -- the CTA-pair (tcgen05 cta_group::2) form of the GEMM engine, for bf16 operands.
+// gemm_tc2.cuh -- the CTA-pair (tcgen05 cta_group::2) form of the GEMM engine, for f16 operands.
 //
 // A cluster of two CTAs on two SMs computes one 256 x BN output tile with M = 256 UMMAs:
 //   CTA r (r = %cluster_ctarank) loads rows [128 r, 128 r + 128) of the A tile and columns
@@ -71,7 +71,7 @@ __device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols
 }
 
 // tcgen05.mma.cta_group::2, issued warp-wide: warp-uniform operands, one elected lane issues.
-__device__ __forceinline__ void umma_bf16_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+__device__ __forceinline__ void umma_f16_pair_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                  uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\t"
@@ -237,8 +237,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     // Warp-wide with one elected issuing lane and descriptors built once (see gemm_tc.cuh).
     if (leader) {
       const WaiterW<true> wt{abort_flag, args.err};
-      const uint32_t idesc = make_idesc_bf16(PM, BN, 0, BMN ? 1 : 0);
-      const uint32_t idesc_ext = make_idesc_bf16(PM, BN, 1, 0);   // A = u^T read MN-major
+      const uint32_t idesc = make_idesc_f16(PM, BN, 0, BMN ? 1 : 0);
+      const uint32_t idesc_ext = make_idesc_f16(PM, BN, 1, 0);   // A = u^T read MN-major
       const uint64_t adesc0 = make_sdesc(smem_u32(smem + L::OFF_A), 16, 1024);
       const uint64_t bdesc0 = BMN ? make_sdesc(smem_u32(smem + L::OFF_B), 8192, 1024)
                                   : make_sdesc(smem_u32(smem + L::OFF_B), 16, 1024);
@@ -264,10 +264,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           if (kb < nkb) {
 #pragma unroll
             for (int kk = 0; kk < kBK / 16; ++kk)
-              umma_bf16_pair_w(d_tmem, adesc0 + aoff + kk * 2u, bdesc0 + boff + kk * B_KSTEP, idesc,
+              umma_f16_pair_w(d_tmem, adesc0 + aoff + kk * 2u, bdesc0 + boff + kk * B_KSTEP, idesc,
                                (kb > 0 || kk > 0) ? 1u : 0u);
           } else {
-            umma_bf16_pair_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
+            umma_f16_pair_w(d_tmem, adesc0_ext + aoff, bdesc0_k + boff, idesc_ext, total > 1 ? 1u : 0u);
           }
           umma_commit_pair_w(&empty[s]);
         }
@@ -325,10 +325,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
               uint4 o;
-              o.x = pack_bf16x2(f[8 * c], f[8 * c + 1]);
-              o.y = pack_bf16x2(f[8 * c + 2], f[8 * c + 3]);
-              o.z = pack_bf16x2(f[8 * c + 4], f[8 * c + 5]);
-              o.w = pack_bf16x2(f[8 * c + 6], f[8 * c + 7]);
+              o.x = pack_f16x2(f[8 * c], f[8 * c + 1]);
+              o.y = pack_f16x2(f[8 * c + 2], f[8 * c + 3]);
+              o.z = pack_f16x2(f[8 * c + 4], f[8 * c + 5]);
+              o.w = pack_f16x2(f[8 * c + 6], f[8 * c + 7]);
               *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) = o;
             }
           }
@@ -342,7 +342,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           ++nstore;
           continue;
         }
-        // direct path (row-major f32 and / or bf16, or transposed outputs)
+        // direct path (row-major f32 and / or f16, or transposed outputs)
         const int ncols = min(32, args.N - nb);
         const int myrow = rbase + lane;
         if (args.out && args.out_trans) {
@@ -356,16 +356,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
             }
           }
         }
-        if (args.out_bf && args.out_bf_trans) {
+        if (args.out_h && args.out_h_trans) {
           if (myrow < args.M) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               if (j >= ncols) break;
-              args.out_bf[(long)(nb + j) * args.ldo_bf + myrow] = __float2bfloat16_rn(f[j]);
+              args.out_h[(long)(nb + j) * args.ldo_h + myrow] = __float2half_rn(f[j]);
             }
           }
         }
-        if ((args.out && !args.out_trans) || (args.out_bf && !args.out_bf_trans)) {
+        if ((args.out && !args.out_trans) || (args.out_h && !args.out_h_trans)) {
           float* st32 = reinterpret_cast<float*>(stg);
 #pragma unroll
           for (int j = 0; j < 32; ++j) st32[lane * 32 + (j ^ lane)] = f[j];
@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
               if (w.add) atomicAdd(dst, x);
               else *dst = args.accumulate ? *dst + x : x;
             }
-            if (args.out_bf && !args.out_bf_trans) args.out_bf[(long)row * args.ldo_bf + nb + lane] = __float2bfloat16_rn(x);
+            if (args.out_h && !args.out_h_trans) args.out_h[(long)row * args.ldo_h + nb + lane] = __float2half_rn(x);
           }
           __syncwarp();
         }

@@ -16,10 +16,10 @@ struct AdapterPrep {
   const float* B = nullptr;            // [out][rank]
   const float* m = nullptr;            // [out] dora-rows magnitude (null: plain LoRA)
   const float* bns = nullptr;          // [out] base row norm^2 + in*eps
-  __nv_bfloat16* a_bf = nullptr;       // [16][in]
-  __nv_bfloat16* at_x = nullptr;       // [in][64]  A^T, extension operand of dx
-  __nv_bfloat16* b_x = nullptr;        // [out][64] B, extension operand of y
-  __nv_bfloat16* bt_bf = nullptr;      // [16][out] B^T
+  __half* a_h = nullptr;       // [16][in]
+  __half* at_x = nullptr;       // [in][64]  A^T, extension operand of dx
+  __half* b_x = nullptr;        // [out][64] B, extension operand of y
+  __half* bt_h = nullptr;      // [16][out] B^T
   float* pt = nullptr;                 // [16][out] (W A^T)^T          (dora)
   float* aat = nullptr;                // [16][16]                      (dora)
   float* nsq = nullptr;                // [out] |W + s B A|_row^2       (dora)
@@ -39,45 +39,45 @@ struct LinearFwd {
   const Weight* w = nullptr;
   const AdapterPrep* ad = nullptr;     // null: plain mul_mat
   const float* bias = nullptr;
-  const __nv_bfloat16* x_bf = nullptr; // [M][in] bf16 input
+  const __half* x_h = nullptr; // [M][in] f16 input
   int64_t M = 0;
   float* y = nullptr;                  // [M][out] f32 output (nullable)
-  __nv_bfloat16* y_bf = nullptr;       // [M][out] bf16 output (nullable)
-  // adapter scratch: ut [16][ut_ld] bf16 (u^T: the K = 16 extension operand, kept for backward)
-  __nv_bfloat16* ut = nullptr;
+  __half* y_h = nullptr;       // [M][out] f16 output (nullable)
+  // adapter scratch: ut [16][ut_ld] f16 (u^T: the K = 16 extension operand, kept for backward)
+  __half* ut = nullptr;
   int64_t ut_ld = 0;
 };
 int linear_forward(Ctx* c, const LinearFwd& f, std::string& err);
-// u = x A^T of an adapter, written as ut = bf16(u)^T [16][ut_ld]
-int lora_u(Ctx* c, const __nv_bfloat16* x_bf, int64_t M, int64_t in, const AdapterPrep& ad, __nv_bfloat16* ut,
+// u = x A^T of an adapter, written as ut = f16(u)^T [16][ut_ld]
+int lora_u(Ctx* c, const __half* x_h, int64_t M, int64_t in, const AdapterPrep& ad, __half* ut,
            int64_t ut_ld, std::string& err);
 
 struct LinearBwd {
   const Weight* w = nullptr;
   const AdapterPrep* ad = nullptr;
   const float* bias = nullptr;
-  const __nv_bfloat16* x_bf = nullptr; // forward input [M][in]
+  const __half* x_h = nullptr; // forward input [M][in]
   const float* y = nullptr;            // forward output [M][out] (needed by dora-rows)
   const float* dy = nullptr;           // upstream gradient [M][out] f32
   bool dz_ready = false;               // dz (and dg for dora) already written by a fused producer
   bool defer_grads = false;            // stop after dx: the caller computes dA / dB / dm later
                                        // (grouped over many adapters) from dz, dg, dut and u^T
   int64_t M = 0;
-  const __nv_bfloat16* ut = nullptr;   // u^T from the forward [16][ut_ld] (adapter)
+  const __half* ut = nullptr;   // u^T from the forward [16][ut_ld] (adapter)
   int64_t ut_ld = 0;
   float* dx = nullptr;                 // [M][in] f32 (nullable)
   int dx_accumulate = 0;
-  __nv_bfloat16* dx_bf = nullptr;      // [M][in] bf16 (nullable; not with dx_accumulate)
+  __half* dx_h = nullptr;      // [M][in] f16 (nullable; not with dx_accumulate)
   float* dA = nullptr;                 // [rank][in]
   float* dB = nullptr;                 // [out][rank]
   float* dm = nullptr;                 // [out] (dora)
   int grad_accumulate = 0;
-  // scratch: dz [M][out] bf16, dg [out], dut [16][ut_ld] bf16,
-  // cb [16][out] bf16, c3 [256]
-  __nv_bfloat16* dz = nullptr;
+  // scratch: dz [M][out] f16, dg [out], dut [16][ut_ld] f16,
+  // cb [16][out] f16, c3 [256]
+  __half* dz = nullptr;
   float* dg = nullptr;
-  __nv_bfloat16* dut = nullptr;
-  __nv_bfloat16* cb = nullptr;
+  __half* dut = nullptr;
+  __half* cb = nullptr;
   float* c3 = nullptr;
 };
 int linear_backward(Ctx* c, const LinearBwd& b, std::string& err);

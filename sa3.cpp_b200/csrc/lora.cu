@@ -4,7 +4,7 @@
 //   z = x W^T + s (x A^T) B^T,   y = g * z + bias,   g = m / sqrt(nsq),
 //   nsq = bns + 2 s t2 + s^2 t3,  t2 = rowsum((W A^T) * B),  t3 = rowsum((B A A^T) * B)
 // and ggml differentiates it (src/train_ckpt.h:400).  The contractions run on the tcgen05 GEMM
-// engine; these kernels do the rank-16 bookkeeping in between: operand packing to bf16, A A^T,
+// engine; these kernels do the rank-16 bookkeeping in between: operand packing to f16, A A^T,
 // the DoRA norm, the backward prologue dz = g * dy with dg = colsum(dy * z), and the DoRA
 // backward terms for dA, dB and dm.  Ranks up to 16 are padded to 16 (zero rows / columns).
 #include "sa3k_common.cuh"
@@ -17,30 +17,30 @@ namespace sa3k {
 
 constexpr int R = 16;   // padded rank
 
-__global__ void cvt_bf16_kernel(const float* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
+__global__ void cvt_f16_kernel(const float* __restrict__ src, int64_t n, __half* __restrict__ dst) {
   pdl_prologue();
   const int64_t n4 = n / 4;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
     const float4 v = reinterpret_cast<const float4*>(src)[i];
     uint2 o;
-    o.x = pack_bf16x2(v.x, v.y);
-    o.y = pack_bf16x2(v.z, v.w);
+    o.x = pack_f16x2(v.x, v.y);
+    o.y = pack_f16x2(v.z, v.w);
     reinterpret_cast<uint2*>(dst)[i] = o;
   }
   for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    dst[i] = __float2bfloat16_rn(src[i]);
+    dst[i] = __float2half_rn(src[i]);
 }
 
 // Adapter operand forms.  A f32 [rank][in], B f32 [out][rank].
-//   a_bf  bf16 [16][in]    (rows >= rank zero)      B operand of u = x A^T, A operand of W A^T
-//   at_x  bf16 [in][64]    A^T in columns 0..15     K-extension B operand of dx
-//   b_x   bf16 [out][64]   s B in columns 0..15     K-extension B operand of y
-//   bt_bf bf16 [16][out]   B^T                      B operand of du = dz B
+//   a_h  f16 [16][in]    (rows >= rank zero)      B operand of u = x A^T, A operand of W A^T
+//   at_x  f16 [in][64]    A^T in columns 0..15     K-extension B operand of dx
+//   b_x   f16 [out][64]   s B in columns 0..15     K-extension B operand of y
+//   bt_h f16 [16][out]   B^T                      B operand of du = dz B
 __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __restrict__ B, int rank, float s,
-                                    int64_t in, int64_t out, __nv_bfloat16* __restrict__ a_bf,
-                                    __nv_bfloat16* __restrict__ at_x, __nv_bfloat16* __restrict__ b_x,
-                                    __nv_bfloat16* __restrict__ bt_bf) {
+                                    int64_t in, int64_t out, __half* __restrict__ a_h,
+                                    __half* __restrict__ at_x, __half* __restrict__ b_x,
+                                    __half* __restrict__ bt_h) {
   pdl_prologue();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -48,15 +48,15 @@ __global__ void prep_adapter_kernel(const float* __restrict__ A, const float* __
     const int64_t i = k / 64;
     const int c = (int)(k % 64);
     const float a = (c < rank) ? A[(int64_t)c * in + i] : 0.f;
-    at_x[k] = __float2bfloat16_rn(a);
-    if (c < R) a_bf[(int64_t)c * in + i] = __float2bfloat16_rn(a);
+    at_x[k] = __float2half_rn(a);
+    if (c < R) a_h[(int64_t)c * in + i] = __float2half_rn(a);
   }
   for (int64_t k = t0; k < out * 64; k += stride) {
     const int64_t o = k / 64;
     const int c = (int)(k % 64);
     const float b = (c < rank) ? B[o * rank + c] : 0.f;
-    b_x[k] = __float2bfloat16_rn(s * b);
-    if (c < R) bt_bf[(int64_t)c * out + o] = __float2bfloat16_rn(b);
+    b_x[k] = __float2half_rn(s * b);
+    if (c < R) bt_h[(int64_t)c * out + o] = __float2half_rn(b);
   }
 }
 
@@ -123,16 +123,16 @@ __global__ void dora_norm_kernel(const float* __restrict__ pt, const float* __re
 
 // ---------------------------------------------------------------- producers fused with the prologue
 // The upstream gradient dy of an adapted linear is produced here and never stored in f32: the
-// kernels write dz = bf16(g * dy) (bf16(dy) without DoRA) and add colsum(dy * z) into dg, with
+// kernels write dz = f16(g * dy) (f16(dy) without DoRA) and add colsum(dy * z) into dg, with
 // z = (y - bias) / g the pre-scale output of the forward.  Thread = 4 columns, block = kFuseTok
 // rows (one f32 atomic per column and block).
 constexpr int kFuseTok = 32;
 constexpr int kGateRows = 16;
 
-__device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4], const float (&gv)[4], bool dora) {
+__device__ __forceinline__ void dz_store4(__half* dz, const float (&dy)[4], const float (&gv)[4], bool dora) {
   uint2 pk;
-  pk.x = pack_bf16x2(dora ? dy[0] * gv[0] : dy[0], dora ? dy[1] * gv[1] : dy[1]);
-  pk.y = pack_bf16x2(dora ? dy[2] * gv[2] : dy[2], dora ? dy[3] * gv[3] : dy[3]);
+  pk.x = pack_f16x2(dora ? dy[0] * gv[0] : dy[0], dora ? dy[1] * gv[1] : dy[1]);
+  pk.y = pack_f16x2(dora ? dy[2] * gv[2] : dy[2], dora ? dy[3] * gv[3] : dy[3]);
   *reinterpret_cast<uint2*>(dz) = pk;
 }
 
@@ -142,7 +142,7 @@ __device__ __forceinline__ void dz_store4(__nv_bfloat16* dz, const float (&dy)[4
 __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restrict__ gx, const float* __restrict__ gate,
                                                           long gstride, int T, int D, int tps,
                                                           const float* __restrict__ y, const float* __restrict__ bias,
-                                                          const float* __restrict__ g, __nv_bfloat16* __restrict__ dz,
+                                                          const float* __restrict__ g, __half* __restrict__ dz,
                                                           float* __restrict__ dg) {
   pdl_prologue();
   __shared__ float4 red[4][128];
@@ -208,20 +208,20 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
   }
 }
 
-// SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (bf16), da (bf16)
+// SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (f16), da (f16)
 // the gradient of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I
 // columns).  Thread = 4 columns of val and the matching 4 of gate, block = kFuseTok rows (two
-// rows' loads first); dz = bf16(g dy) and, for DoRA, dg += colsum(dy (y - bias) / g).
-__device__ __forceinline__ void bf16x4(const uint2 w, float (&v)[4]) {
-  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
-  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+// rows' loads first); dz = f16(g dy) and, for DoRA, dg += colsum(dy (y - bias) / g).
+__device__ __forceinline__ void f16x4(const uint2 w, float (&v)[4]) {
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
   v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
 }
 
-__global__ void swiglu_bwd_dz_kernel(const __nv_bfloat16* __restrict__ da, const __nv_bfloat16* __restrict__ f, int T,
+__global__ void swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half* __restrict__ f, int T,
                                      int I,
                                      const float* __restrict__ bias, const float* __restrict__ g,
-                                     __nv_bfloat16* __restrict__ dz, float* __restrict__ dg) {
+                                     __half* __restrict__ dz, float* __restrict__ dg) {
   pdl_prologue();
   const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
@@ -245,7 +245,7 @@ __global__ void swiglu_bwd_dz_kernel(const __nv_bfloat16* __restrict__ da, const
 #pragma unroll
     for (int u = 0; u < 2; ++u) {                    // both rows' loads first
       const int t = min(tb + u, t1 - 1);
-      const __nv_bfloat16* fr = f + (long)t * 2 * I;
+      const __half* fr = f + (long)t * 2 * I;
       v2[u] = *reinterpret_cast<const uint2*>(fr + j);
       g2[u] = *reinterpret_cast<const uint2*>(fr + I + j);
       d2[u] = *reinterpret_cast<const uint2*>(da + (long)t * I + j);
@@ -255,9 +255,9 @@ __global__ void swiglu_bwd_dz_kernel(const __nv_bfloat16* __restrict__ da, const
       const int t = tb + u;
       if (t >= t1) break;
       float vv[4], gg[4], dd[4];
-      bf16x4(v2[u], vv);
-      bf16x4(g2[u], gg);
-      bf16x4(d2[u], dd);
+      f16x4(v2[u], vv);
+      f16x4(g2[u], gg);
+      f16x4(d2[u], dd);
       float dv[4], dgl[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -265,7 +265,7 @@ __global__ void swiglu_bwd_dz_kernel(const __nv_bfloat16* __restrict__ da, const
         dv[e] = dd[e] * gg[e] * sg;
         dgl[e] = dd[e] * vv[e] * sg * (1.f + gg[e] * (1.f - sg));
       }
-      __nv_bfloat16* zr = dz + (long)t * 2 * I;
+      __half* zr = dz + (long)t * 2 * I;
       dz_store4(zr + j, dv, gvv, dora);
       dz_store4(zr + I + j, dgl, ggg, dora);
       if (dora) {
@@ -298,14 +298,14 @@ __global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
   for (int k = t0; k < nin; k += stride) {
     const int i = k >> 6, c = k & 63;
     const float a = (c < d.rank) ? d.A[(int64_t)c * d.in + i] : 0.f;
-    d.at_x[k] = __float2bfloat16_rn(a);
-    if (c < R) d.a_bf[(int64_t)c * d.in + i] = __float2bfloat16_rn(a);
+    d.at_x[k] = __float2half_rn(a);
+    if (c < R) d.a_h[(int64_t)c * d.in + i] = __float2half_rn(a);
   }
   for (int k = t0; k < nout; k += stride) {
     const int o = k >> 6, c = k & 63;
     const float b = (c < d.rank) ? d.B[(int64_t)o * d.rank + c] : 0.f;
-    d.b_x[k] = __float2bfloat16_rn(d.s * b);
-    if (c < R) d.bt_bf[(int64_t)c * d.out + o] = __float2bfloat16_rn(b);
+    d.b_x[k] = __float2half_rn(d.s * b);
+    if (c < R) d.bt_h[(int64_t)c * d.out + o] = __float2half_rn(b);
   }
 }
 
@@ -366,12 +366,12 @@ __global__ void dora_norm_all_kernel(const PrepDesc* __restrict__ descs) {
 }
 
 // Backward prologue over dy[S][out] (one thread per column, TOK rows per block):
-//   dz = bf16(g * dy) ;  dg[o] += sum_t dy[t][o] * (y[t][o] - bias[o]) / g[o]   (dora only)
-// With g == null this is the plain f32 -> bf16 conversion of dy.
+//   dz = f16(g * dy) ;  dg[o] += sum_t dy[t][o] * (y[t][o] - bias[o]) / g[o]   (dora only)
+// With g == null this is the plain f32 -> f16 conversion of dy.
 constexpr int kProTok = 32;
 __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* __restrict__ y,
                                     const float* __restrict__ bias, const float* __restrict__ g,
-                                    int64_t S, int64_t out, __nv_bfloat16* __restrict__ dz,
+                                    int64_t S, int64_t out, __half* __restrict__ dz,
                                     float* __restrict__ dg) {
   pdl_prologue();
   const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -379,14 +379,14 @@ __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* _
   const int64_t t0 = (int64_t)blockIdx.y * kProTok;
   const int64_t t1 = t0 + kProTok < S ? t0 + kProTok : S;
   if (!g) {
-    for (int64_t t = t0; t < t1; ++t) dz[t * out + o] = __float2bfloat16_rn(dy[t * out + o]);
+    for (int64_t t = t0; t < t1; ++t) dz[t * out + o] = __float2half_rn(dy[t * out + o]);
     return;
   }
   const float go = g[o], bo = bias ? bias[o] : 0.f, inv = 1.f / go;
   float acc = 0.f;
   for (int64_t t = t0; t < t1; ++t) {
     const float d = dy[t * out + o];
-    dz[t * out + o] = __float2bfloat16_rn(d * go);
+    dz[t * out + o] = __float2half_rn(d * go);
     acc = fmaf(d, (y[t * out + o] - bo) * inv, acc);
   }
   atomicAdd(dg + o, acc);
@@ -396,7 +396,7 @@ __global__ void bwd_prologue_kernel(const float* __restrict__ dy, const float* _
 //   dm  = dg / sqrt(nsq)                      dnsq = -0.5 dg g / nsq
 //   dt2 = 2 s dnsq, dt3 = s^2 dnsq
 //   dB[o][r] += dt2 P[o][r] + 2 dt3 (B AAt)[o][r]
-//   cb[r][o] = bf16(dt2 B[o][r])   (A operand of dA += cb W, a rank-16 quant GEMM)
+//   cb[r][o] = f16(dt2 B[o][r])   (A operand of dA += cb W, a rank-16 quant GEMM)
 //   c3[r][k] += dt3 B[o][r] B[o][k]           (dA += 2 c3 A afterwards)
 // 128 rows per block.  Phase 1: one thread per row (dm, dB, cb; the row's dt3 B[o][:] and B[o][:]
 // go to shared memory).  Phase 2: thread (r, k), r <= k < R, sums dt3 B[o][r] B[o][k] over the
@@ -407,7 +407,7 @@ __device__ __forceinline__ void dora_bwd_rows(int blk, const float* __restrict__
                                               const float* __restrict__ nsq, const float* __restrict__ g,
                                               const float* __restrict__ dg, float s, float* __restrict__ dm,
                                               int dm_accumulate, float* __restrict__ dB,
-                                              __nv_bfloat16* __restrict__ cb, float* __restrict__ c3) {
+                                              __half* __restrict__ cb, float* __restrict__ c3) {
   __shared__ float saat[R * R];
   __shared__ float sb[kDoraRows][R + 1];    // B[o][:]          (+1: no bank conflicts on columns)
   __shared__ float sbt[kDoraRows][R + 1];   // dt3[o] B[o][:]
@@ -434,7 +434,7 @@ __device__ __forceinline__ void dora_bwd_rows(int blk, const float* __restrict__
 #pragma unroll
       for (int k = 0; k < R; ++k) bar = fmaf(b[k], saat[k * R + r], bar);
       if (r < rank) dB[o * rank + r] += dt2 * pt[(int64_t)r * out + o] + 2.f * dt3 * bar;
-      cb[(int64_t)r * out + o] = __float2bfloat16_rn(dt2 * b[r]);
+      cb[(int64_t)r * out + o] = __float2half_rn(dt2 * b[r]);
     }
   }
 #pragma unroll
@@ -460,7 +460,7 @@ __device__ __forceinline__ void dora_bwd_rows(int blk, const float* __restrict__
 __global__ void __launch_bounds__(kDoraRows) dora_bwd_kernel(
     const float* __restrict__ pt, const float* __restrict__ B, int rank, int64_t out, const float* __restrict__ aat,
     const float* __restrict__ nsq, const float* __restrict__ g, const float* __restrict__ dg, float s,
-    float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __nv_bfloat16* __restrict__ cb,
+    float* __restrict__ dm, int dm_accumulate, float* __restrict__ dB, __half* __restrict__ cb,
     float* __restrict__ c3) {
   pdl_prologue();
   dora_bwd_rows(blockIdx.x, pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_accumulate, dB, cb, c3);
@@ -517,18 +517,18 @@ static unsigned grid1d(int64_t n, int threads, int cap = 148 * 16) {
   return (unsigned)(b < 1 ? 1 : b);
 }
 
-int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err) {
-  ProfScope prof_(c, "cvt_bf16");
-  launch_pdl(c, cvt_bf16_kernel, grid1d(n / 4 + 1, 256), 256, 0, src, n, dst);
-  return check_launch("cvt_bf16", err);
+int k_cvt_f16(Ctx* c, const float* src, int64_t n, __half* dst, std::string& err) {
+  ProfScope prof_(c, "cvt_f16");
+  launch_pdl(c, cvt_f16_kernel, grid1d(n / 4 + 1, 256), 256, 0, src, n, dst);
+  return check_launch("cvt_f16", err);
 }
 
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, float s, int64_t in, int64_t out,
-                   __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
+                   __half* a_h, __half* at_x, __half* b_x, __half* bt_h,
                    std::string& err) {
   ProfScope prof_(c, "prep_adapter");
-  launch_pdl(c, prep_adapter_kernel, grid1d((in + out) * 64, 256), 256, 0, A, B, rank, s, in, out, a_bf, at_x, b_x,
-                                                                             bt_bf);
+  launch_pdl(c, prep_adapter_kernel, grid1d((in + out) * 64, 256), 256, 0, A, B, rank, s, in, out, a_h, at_x, b_x,
+                                                                             bt_h);
   return check_launch("prep_adapter", err);
 }
 
@@ -546,7 +546,7 @@ int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, 
 }
 
 int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
-                   int64_t out, __nv_bfloat16* dz, float* dg, std::string& err) {
+                   int64_t out, __half* dz, float* dg, std::string& err) {
   ProfScope prof_(c, "bwd_prologue");
   dim3 grid((unsigned)((out + 255) / 256), (unsigned)((S + kProTok - 1) / kProTok));
   launch_pdl(c, bwd_prologue_kernel, grid, 256, 0, dy, y, bias, g, S, out, dz, dg);
@@ -555,7 +555,7 @@ int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, c
 
 int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
-               float* dB, __nv_bfloat16* cb, float* c3, std::string& err) {
+               float* dB, __half* cb, float* c3, std::string& err) {
   ProfScope prof_(c, "dora_bwd");
   launch_pdl(c, dora_bwd_kernel, (unsigned)((out + kDoraRows - 1) / kDoraRows), kDoraRows, 0, 
       pt, B, rank, out, aat, nsq, g, dg, s, dm, dm_acc, dB, cb, c3);
@@ -563,7 +563,7 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
 }
 
 int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
-                  const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err) {
+                  const float* bias, const float* g, __half* dz, float* dg, std::string& err) {
   if (D % 4) { err = "gate: the width must be a multiple of 4"; return 1; }
   const unsigned gx_blocks = (unsigned)((D / 4 + 127) / 128), nchunk = (unsigned)((T + kGateRows - 1) / kGateRows);
   const unsigned gy = std::max(1u, std::min(nchunk, (unsigned)(2 * c->sm_count) / gx_blocks));
@@ -574,9 +574,9 @@ int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int 
   return check_launch("gate_bwd_dz", err);
 }
 
-int k_swiglu_bwd_dz(Ctx* c, const __nv_bfloat16* da, const __nv_bfloat16* f, int T, int I, const float* bias,
+int k_swiglu_bwd_dz(Ctx* c, const __half* da, const __half* f, int T, int I, const float* bias,
                     const float* g,
-                    __nv_bfloat16* dz, float* dg, std::string& err) {
+                    __half* dz, float* dg, std::string& err) {
   if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 2 * I, c->stream) != cudaSuccess) return check_launch("memset", err);

@@ -13,7 +13,7 @@
 //
 // On the device: one P = W A^T GEMM per 16 ranks of the chain, one A A^T kernel, one fold kernel
 // (one thread per output row walks the chain) that writes b and the extension operand
-// B'' = s_k g_k B_k / b in bf16.  The forward is then the fused LoRA GEMM of the training path:
+// B'' = s_k g_k B_k / b in f16.  The forward is then the fused LoRA GEMM of the training path:
 // u = x A_cat^T (rank <= 16 in all), y = b * (x W^T + u B''^T) + bias in one GEMM.  A chain of more
 // than 16 ranks, or with a row where b = 0, runs the base GEMM with column scale b and adds each
 // 16-rank group u_g (s g B)_g^T with one more accumulating K = 16 GEMM.
@@ -66,7 +66,7 @@ __global__ void aat_cat_kernel(const float* __restrict__ A, int R, int64_t in, f
 // b[o] and B''[group][o][64] (columns of the group's 16 ranks; the rest zero).
 __global__ void chain_fold_kernel(const __grid_constant__ ChainArgs a, const float* __restrict__ pt,
                                   const float* __restrict__ aat, const float* __restrict__ nsq0, int64_t out,
-                                  float* __restrict__ bsc, __nv_bfloat16* __restrict__ bx, int* __restrict__ zero_rows) {
+                                  float* __restrict__ bsc, __half* __restrict__ bx, int* __restrict__ zero_rows) {
   const int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (o >= out) return;
   const int n = a.n, R = a.R;
@@ -117,7 +117,7 @@ __global__ void chain_fold_kernel(const __grid_constant__ ChainArgs a, const flo
       if (c < 16 && idx < R)
         for (int k = 0; k < n; ++k)
           if (idx >= a.t[k].col && idx < a.t[k].col + a.t[k].rank) v = a.t[k].s * g[k] * bv[idx] * inv;
-      bx[((int64_t)gi * out + o) * 64 + c] = __float2bfloat16_rn(v);
+      bx[((int64_t)gi * out + o) * 64 + c] = __float2half_rn(v);
     }
 }
 
@@ -127,8 +127,8 @@ struct LoraChain {
   int R = 0, groups = 0, n = 0;
   bool any_dora = false, fused = false;
   int64_t in = 0, out = 0;
-  __nv_bfloat16* a_bf = nullptr;   // [16 groups][in] bf16 (A_cat, zero rows past R)
-  __nv_bfloat16* bx = nullptr;     // [groups][out][64] bf16 (s g B, / b when fused)
+  __half* a_h = nullptr;   // [16 groups][in] f16 (A_cat, zero rows past R)
+  __half* bx = nullptr;     // [groups][out][64] f16 (s g B, / b when fused)
   float* bsc = nullptr;            // [out] base scale b (any dora)
   void* mem = nullptr;
   ~LoraChain() {
@@ -154,7 +154,7 @@ static int chain_build(Ctx* c, const Weight* w, const sa3k_chain_term* terms, in
   const int groups = (R + 15) / 16;
   a.n = n; a.R = R; a.groups = groups; a.any_dora = any_dora ? 1 : 0;
   ch.R = R; ch.groups = groups; ch.n = n; ch.any_dora = any_dora; ch.in = in; ch.out = out;
-  // device memory: a_bf, bx, bsc, A_cat f32, P^T f32, A A^T, nsq0, the zero-row counter
+  // device memory: a_h, bx, bsc, A_cat f32, P^T f32, A A^T, nsq0, the zero-row counter
   auto al = [](size_t b) { return (b + 255) & ~(size_t)255; };
   const size_t b_abf = al((size_t)16 * groups * in * 2), b_bx = al((size_t)groups * out * 64 * 2), b_bsc = al(out * 4);
   const size_t b_acat = al((size_t)R * in * 4), b_pt = al((size_t)16 * groups * out * 4), b_aat = al((size_t)R * R * 4);
@@ -165,8 +165,8 @@ static int chain_build(Ctx* c, const Weight* w, const sa3k_chain_term* terms, in
     return 1;
   }
   char* q = static_cast<char*>(ch.mem);
-  ch.a_bf = reinterpret_cast<__nv_bfloat16*>(q); q += b_abf;
-  ch.bx = reinterpret_cast<__nv_bfloat16*>(q); q += b_bx;
+  ch.a_h = reinterpret_cast<__half*>(q); q += b_abf;
+  ch.bx = reinterpret_cast<__half*>(q); q += b_bx;
   ch.bsc = reinterpret_cast<float*>(q); q += b_bsc;
   float* acat = reinterpret_cast<float*>(q); q += b_acat;
   float* pt = reinterpret_cast<float*>(q); q += b_pt;
@@ -174,19 +174,19 @@ static int chain_build(Ctx* c, const Weight* w, const sa3k_chain_term* terms, in
   float* nsq0 = reinterpret_cast<float*>(q); q += b_nsq;
   int* zero_rows = reinterpret_cast<int*>(q);
   cudaStream_t st = c->stream;
-  if (cudaMemsetAsync(ch.a_bf, 0, b_abf, st) != cudaSuccess || cudaMemsetAsync(zero_rows, 0, sizeof(int), st) != cudaSuccess)
+  if (cudaMemsetAsync(ch.a_h, 0, b_abf, st) != cudaSuccess || cudaMemsetAsync(zero_rows, 0, sizeof(int), st) != cudaSuccess)
     return check_launch("memset", err);
   for (int k = 0; k < n; ++k)
     if (cudaMemcpyAsync(acat + (int64_t)a.t[k].col * in, terms[k].A, sizeof(float) * terms[k].rank * in,
                         cudaMemcpyDeviceToDevice, st) != cudaSuccess)
       return check_launch("copy", err);
-  if (k_cvt_bf16(c, acat, (int64_t)R * in, ch.a_bf, err)) return 1;
+  if (k_cvt_f16(c, acat, (int64_t)R * in, ch.a_h, err)) return 1;
   if (any_dora) {
     if (weight_row_norms(c, w, 1e-12f, nsq0, nullptr, err)) return 1;   // |W|_row^2 + in eps
     for (int gi = 0; gi < groups; ++gi) {   // P^T rows of group gi = (W A_g^T)^T
       AdapterPrep p;
       p.in = in; p.out = out; p.rank = 16;
-      p.a_bf = ch.a_bf + (int64_t)gi * 16 * in;
+      p.a_h = ch.a_h + (int64_t)gi * 16 * in;
       p.pt = pt + (int64_t)gi * 16 * out;
       if (adapter_dora_p(c, w, p, err)) return 1;
     }
@@ -211,17 +211,17 @@ static int chain_build(Ctx* c, const Weight* w, const sa3k_chain_term* terms, in
   return 0;
 }
 
-static int chain_forward(Ctx* c, const Weight* w, const LoraChain& ch, const float* bias, const __nv_bfloat16* x_bf,
-                         int64_t M, float* y, __nv_bfloat16* u_buf, int64_t u_ld, std::string& err) {
+static int chain_forward(Ctx* c, const Weight* w, const LoraChain& ch, const float* bias, const __half* x_h,
+                         int64_t M, float* y, __half* u_buf, int64_t u_ld, std::string& err) {
   if (ch.fused) {
     AdapterPrep p;   // the training path's fused forward with the chain's operands
     p.in = ch.in; p.out = ch.out; p.rank = 16; p.s = 1.f;
-    p.a_bf = ch.a_bf;
+    p.a_h = ch.a_h;
     p.b_x = ch.bx;
-    if (lora_u(c, x_bf, M, ch.in, p, u_buf, u_ld, err)) return 1;
+    if (lora_u(c, x_h, M, ch.in, p, u_buf, u_ld, err)) return 1;
     GemmDesc g;
     g.M = (int)M; g.N = (int)ch.out; g.K = (int)ch.in;
-    g.a = x_bf; g.lda = ch.in;
+    g.a = x_h; g.lda = ch.in;
     g.bsrc = kB_WEIGHT_NT; g.w = w;
     g.ext_at = u_buf; g.ld_ext = u_ld; g.ext_b = ch.bx;
     g.col_scale = ch.any_dora ? ch.bsc : nullptr;
@@ -235,9 +235,9 @@ static int chain_forward(Ctx* c, const Weight* w, const LoraChain& ch, const flo
   {
     GemmDesc g;
     g.M = (int)M; g.N = RP; g.K = (int)ch.in;
-    g.a = x_bf; g.lda = ch.in;
-    g.bsrc = kB_BF16_KMAJOR; g.b = ch.a_bf; g.ldb = ch.in;
-    g.out_bf = u_buf; g.ldo_bf = RP;
+    g.a = x_h; g.lda = ch.in;
+    g.bsrc = kB_F16_KMAJOR; g.b = ch.a_h; g.ldb = ch.in;
+    g.out_h = u_buf; g.ldo_h = RP;
     g.bn = 16;
     g.name = "lora.u";
     if (gemm(c, g, err)) return 1;
@@ -245,7 +245,7 @@ static int chain_forward(Ctx* c, const Weight* w, const LoraChain& ch, const flo
   {
     GemmDesc g;
     g.M = (int)M; g.N = (int)ch.out; g.K = (int)ch.in;
-    g.a = x_bf; g.lda = ch.in;
+    g.a = x_h; g.lda = ch.in;
     g.bsrc = kB_WEIGHT_NT; g.w = w;
     g.col_scale = ch.any_dora ? ch.bsc : nullptr;
     g.col_bias = bias;
@@ -257,7 +257,7 @@ static int chain_forward(Ctx* c, const Weight* w, const LoraChain& ch, const flo
     GemmDesc g;
     g.M = (int)M; g.N = (int)ch.out; g.K = 16;
     g.a = u_buf + 16 * gi; g.lda = RP;
-    g.bsrc = kB_BF16_KMAJOR; g.b = ch.bx + (int64_t)gi * ch.out * 64; g.ldb = 64;
+    g.bsrc = kB_F16_KMAJOR; g.b = ch.bx + (int64_t)gi * ch.out * 64; g.ldb = 64;
     g.out = y; g.ldo = ch.out; g.accumulate = 1;
     g.name = "lora.chain";
     if (gemm(c, g, err)) return 1;
@@ -318,12 +318,12 @@ int sa3k_linear_fwd_chain(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_lora_c
   cudaSetDevice(c->device);
   std::string e;
   const int64_t in = w->w.in, s_pad = (S + 63) / 64 * 64;
-  __nv_bfloat16* x_bf = static_cast<__nv_bfloat16*>(scratch_get(c, kSlotChainX, sizeof(__nv_bfloat16) * S * in, e));
-  __nv_bfloat16* u = x_bf ? static_cast<__nv_bfloat16*>(scratch_get(c, kSlotChainU, sizeof(__nv_bfloat16) * 64 * s_pad, e))
+  __half* x_h = static_cast<__half*>(scratch_get(c, kSlotChainX, sizeof(__half) * S * in, e));
+  __half* u = x_h ? static_cast<__half*>(scratch_get(c, kSlotChainU, sizeof(__half) * 64 * s_pad, e))
                           : nullptr;
-  if (!x_bf || !u) return lfail(err, err_len, e);
-  if (k_cvt_bf16(c, x, S * in, x_bf, e)) return lfail(err, err_len, e);
-  if (chain_forward(c, &w->w, chain->ch, bias, x_bf, S, y, u, chain->ch.fused ? s_pad : 16 * chain->ch.groups, e))
+  if (!x_h || !u) return lfail(err, err_len, e);
+  if (k_cvt_f16(c, x, S * in, x_h, e)) return lfail(err, err_len, e);
+  if (chain_forward(c, &w->w, chain->ch, bias, x_h, S, y, u, chain->ch.fused ? s_pad : 16 * chain->ch.groups, e))
     return lfail(err, err_len, e);
   return 0;
 }

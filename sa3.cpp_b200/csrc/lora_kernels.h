@@ -14,17 +14,17 @@ struct PrepDesc {
   int rank, dora;
   float s;
   int64_t in, out;
-  __nv_bfloat16 *a_bf, *at_x, *b_x, *bt_bf;
+  __half *a_h, *at_x, *b_x, *bt_h;
   float *pt, *aat, *nsq, *g;
   // gradients (grouped DoRA backward): dg [out] in, dm [out] / dB [out][rank] / dA [rank][in]
-  // accumulated, cb [16][out] bf16 and c3 [16][16] (zeroed before) out
+  // accumulated, cb [16][out] f16 and c3 [16][16] (zeroed before) out
   const float* dg;
   float *dm, *dB, *dA;
-  __nv_bfloat16* cb;
+  __half* cb;
   float* c3;
 };
 
-int k_cvt_bf16(Ctx* c, const float* src, int64_t n, __nv_bfloat16* dst, std::string& err);
+int k_cvt_f16(Ctx* c, const float* src, int64_t n, __half* dst, std::string& err);
 // grouped over n adapters (descs in device memory): operand packing, A A^T, DoRA norm
 int k_prep_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_aat_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
@@ -33,22 +33,22 @@ int k_dora_norm_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::
 int k_dora_bwd_all(Ctx* c, const PrepDesc* descs, int n, int64_t max_out, std::string& err);
 int k_dora_da_c3_all(Ctx* c, const PrepDesc* descs, int n, std::string& err);
 int k_prep_adapter(Ctx* c, const float* A, const float* B, int rank, float s, int64_t in, int64_t out,
-                   __nv_bfloat16* a_bf, __nv_bfloat16* at_x, __nv_bfloat16* b_x, __nv_bfloat16* bt_bf,
+                   __half* a_h, __half* at_x, __half* b_x, __half* bt_h,
                    std::string& err);
 int k_aat(Ctx* c, const float* A, int rank, int64_t in, float* aat, std::string& err);
 int k_dora_norm(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                 const float* bns, const float* m, float s, float* nsq, float* g, std::string& err);
 // Producers of an adapted linear's output gradient fused with its backward prologue: write
-// dz = bf16(g * dy) and dg = colsum(dy * (y - bias) / g) (dg zeroed first; g null: dz = bf16(dy)).
+// dz = f16(g * dy) and dg = colsum(dy * (y - bias) / g) (dg zeroed first; g null: dz = f16(dy)).
 int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int T, int D, int tps, const float* y,
-                  const float* bias, const float* g, __nv_bfloat16* dz, float* dg, std::string& err);
-int k_swiglu_bwd_dz(Ctx* c, const __nv_bfloat16* da, const __nv_bfloat16* f, int T, int I, const float* bias,
-                    const float* g, __nv_bfloat16* dz, float* dg, std::string& err);
+                  const float* bias, const float* g, __half* dz, float* dg, std::string& err);
+int k_swiglu_bwd_dz(Ctx* c, const __half* da, const __half* f, int T, int I, const float* bias,
+                    const float* g, __half* dz, float* dg, std::string& err);
 int k_bwd_prologue(Ctx* c, const float* dy, const float* y, const float* bias, const float* g, int64_t S,
-                   int64_t out, __nv_bfloat16* dz, float* dg, std::string& err);
+                   int64_t out, __half* dz, float* dg, std::string& err);
 int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, const float* aat,
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
-               float* dB, __nv_bfloat16* cb, float* c3, std::string& err);
+               float* dB, __half* cb, float* c3, std::string& err);
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err);
 
 // adamw.cu

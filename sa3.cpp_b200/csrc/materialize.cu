@@ -6,7 +6,7 @@
 //   V     = W + s * (B A)             or, for -xs, W + s * (U M) V^T      f32 [out][in]
 //   rows  rs[o] = m_r[o] / sqrt(sum_i V^2 + in * 1e-12)    (dora-rows: m, bora: m_r; else 1)
 //   cols  cs[i] = m_c[i] / sqrt(sum_o (rs V)^2 + out * 1e-12)  (dora-cols: m, bora: m_c; else 1)
-//   W_eff = rs[o] * V * cs[i], kept as the bf16 operand of the GEMMs
+//   W_eff = rs[o] * V * cs[i], kept as the f16 operand of the GEMMs
 //   y     = x W_eff^T + bias                                 (tcgen05 GEMM)
 // Backward:
 //   dx    = dy W_eff                                         (tcgen05 GEMM, W_eff read MN-major)
@@ -184,10 +184,10 @@ __global__ void mat_colfac_kernel(const double* __restrict__ csq, const double* 
   }
 }
 
-// W_eff = rs[o] V cs[i] as bf16 (the GEMM operand) and, when asked, f32.
+// W_eff = rs[o] V cs[i] as f16 (the GEMM operand) and, when asked, f32.
 __global__ void mat_weff_kernel(const float* __restrict__ V, const float* __restrict__ rs,
                                 const float* __restrict__ cs, int64_t out, int64_t in,
-                                __nv_bfloat16* __restrict__ wb, float* __restrict__ wf) {
+                                __half* __restrict__ wb, float* __restrict__ wf) {
   const int64_t n4 = out * in / 4;
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n4; k += (int64_t)gridDim.x * blockDim.x) {
     const int64_t e = 4 * k, o = e / in, i = e % in;
@@ -197,13 +197,13 @@ __global__ void mat_weff_kernel(const float* __restrict__ V, const float* __rest
     const float4 y = make_float4(r * v.x * c.x, r * v.y * c.y, r * v.z * c.z, r * v.w * c.w);
     if (wf) reinterpret_cast<float4*>(wf)[k] = y;
     uint2 p;
-    p.x = pack_bf16x2(y.x, y.y);
-    p.y = pack_bf16x2(y.z, y.w);
+    p.x = pack_f16x2(y.x, y.y);
+    p.y = pack_f16x2(y.z, y.w);
     reinterpret_cast<uint2*>(wb)[k] = p;
   }
 }
 
-// The row pass of the backward: dD = s dV as bf16 (the operand of the dB / dA GEMMs):
+// The row pass of the backward: dD = s dV as f16 (the operand of the dB / dA GEMMs):
 //   dR = cols ? cs[i] (G - rs V tcn[i]) : G
 //   rows: t = sum_i dR V, dmr[o] += t / rn, dV = rs (dR - V t / rn^2), else dV = dR
 // A block of 128 threads takes two rows, its threads spread over the columns (many warps per SM
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(const float* __r
                                                                 const float* __restrict__ tcn, int64_t out,
                                                                 int64_t in, float s, int rows, int cols,
                                                                 float* __restrict__ dmr,
-                                                                __nv_bfloat16* __restrict__ dDb) {
+                                                                __half* __restrict__ dDb) {
   __shared__ double red_t[kRbWarps][kRbRows];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t o0 = (int64_t)blockIdx.x * kRbRows;
@@ -285,8 +285,8 @@ __global__ void __launch_bounds__(kRbThreads) mat_rowbwd_kernel(const float* __r
 #pragma unroll
       for (int c = 0; c < 4; ++c) d[c] = s * (rows ? ro[u] * (d[c] - vx[c] * t_over[u]) : d[c]);
       uint2 pk;
-      pk.x = pack_bf16x2(d[0], d[1]);
-      pk.y = pack_bf16x2(d[2], d[3]);
+      pk.x = pack_f16x2(d[0], d[1]);
+      pk.y = pack_f16x2(d[2], d[3]);
       *reinterpret_cast<uint2*>(dDb + (o0 + u) * in + i) = pk;
     }
   }
@@ -309,22 +309,22 @@ __global__ void mat_dm_xs_kernel(const float* __restrict__ U, const float* __res
   }
 }
 
-// dst[o][s] = src[s][o] for bf16 src [S][out] -> dst [out][ld] (ld even), 64 x 64 tiles: every
-// thread moves bf16 pairs, so a warp reads and writes 128 contiguous bytes (even widths).
-__global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src, int64_t S, int64_t out,
-                                           __nv_bfloat16* __restrict__ dst, int64_t ld) {
-  __shared__ __nv_bfloat16 t[64][66];   // [s][o], padded
+// dst[o][s] = src[s][o] for f16 src [S][out] -> dst [out][ld] (ld even), 64 x 64 tiles: every
+// thread moves f16 pairs, so a warp reads and writes 128 contiguous bytes (even widths).
+__global__ void transpose_f16_kernel(const __half* __restrict__ src, int64_t S, int64_t out,
+                                           __half* __restrict__ dst, int64_t ld) {
+  __shared__ __half t[64][66];   // [s][o], padded
   const int64_t s0 = (int64_t)blockIdx.x * 64, o0 = (int64_t)blockIdx.y * 64;
   const int tx = threadIdx.x;
-  const __nv_bfloat16 zero = __float2bfloat16_rn(0.f);
+  const __half zero = __float2half_rn(0.f);
   for (int k = threadIdx.y; k < 64; k += blockDim.y) {
     const int64_t s = s0 + k, o = o0 + 2 * tx;
-    __nv_bfloat162 v;
+    __half2 v;
     v.x = zero;
     v.y = zero;
     if (s < S && o < out) {
       if ((out & 1) == 0) {
-        v = *reinterpret_cast<const __nv_bfloat162*>(src + s * out + o);
+        v = *reinterpret_cast<const __half2*>(src + s * out + o);
       } else {   // odd widths: rows are not 4-byte aligned
         v.x = src[s * out + o];
         if (o + 1 < out) v.y = src[s * out + o + 1];
@@ -338,10 +338,10 @@ __global__ void transpose_bf16_bf16_kernel(const __nv_bfloat16* __restrict__ src
     const int64_t o = o0 + k, s = s0 + 2 * tx;
     if (o >= out || s >= S) continue;
     if (s + 1 < S) {
-      __nv_bfloat162 v;
+      __half2 v;
       v.x = t[2 * tx][k];
       v.y = t[2 * tx + 1][k];
-      *reinterpret_cast<__nv_bfloat162*>(dst + o * ld + s) = v;   // ld and s even
+      *reinterpret_cast<__half2*>(dst + o * ld + s) = v;   // ld and s even
     } else {
       dst[o * ld + s] = t[2 * tx][k];
     }
@@ -360,17 +360,17 @@ __global__ void mat_col_norms_kernel(const Weight w, float* __restrict__ nrm) {
   nrm[i] = (float)sqrt(a);
 }
 
-// Per-step bf16 operands of the weight-gradient GEMMs: Qb [r][in] = Q (A, or V^T for -xs) and,
+// Per-step f16 operands of the weight-gradient GEMMs: Qb [r][in] = Q (A, or V^T for -xs) and,
 // for the standard families, Btb [r][out] = B^T.
 __global__ void mat_pack_kernel(const float* __restrict__ Q, const float* __restrict__ B, int64_t out, int64_t in,
-                                int r, __nv_bfloat16* __restrict__ Qb, __nv_bfloat16* __restrict__ Btb) {
+                                int r, __half* __restrict__ Qb, __half* __restrict__ Btb) {
   const int64_t n1 = (int64_t)r * in, n = n1 + (B ? (int64_t)r * out : 0);
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x) {
     if (k < n1) {
-      Qb[k] = __float2bfloat16_rn(Q[k]);
+      Qb[k] = __float2half_rn(Q[k]);
     } else {
       const int64_t q = k - n1, j = q / out, o = q % out;
-      Btb[q] = __float2bfloat16_rn(B[o * r + j]);
+      Btb[q] = __float2half_rn(B[o * r + j]);
     }
   }
 }
@@ -447,11 +447,11 @@ int mat_check(const sa3k_weight* w, const sa3k_mat_adapter* ad, int64_t S, MatPl
   return 0;
 }
 
-// The target form of one call's adapter, its buffers and the call's scratch (x, dy as bf16, G,
+// The target form of one call's adapter, its buffers and the call's scratch (x, dy as f16, G,
 // the transposed dy, dD) carved from one context scratch slot.
 struct MatCall {
   MatTarget t;
-  __nv_bfloat16 *xb = nullptr, *dyb = nullptr, *dyt = nullptr, *dDb = nullptr;
+  __half *xb = nullptr, *dyb = nullptr, *dyt = nullptr, *dDb = nullptr;
   float* G = nullptr;
   int64_t ldt = 0;
 };
@@ -477,12 +477,12 @@ bool mat_prepare(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatP
   uint8_t* base = static_cast<uint8_t*>(scratch_get(c, kSlotMat, tb + xb + extra, err));
   if (!base) return false;
   mat_target_bind(t, base);
-  mc.xb = reinterpret_cast<__nv_bfloat16*>(base + tb);
+  mc.xb = reinterpret_cast<__half*>(base + tb);
   if (bwd) {
     uint8_t* q = base + tb + xb;
-    mc.dyb = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)(S * out));
-    mc.dyt = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)(out * mc.ldt));
-    mc.dDb = reinterpret_cast<__nv_bfloat16*>(q); q += al(2 * (size_t)wn);
+    mc.dyb = reinterpret_cast<__half*>(q); q += al(2 * (size_t)(S * out));
+    mc.dyt = reinterpret_cast<__half*>(q); q += al(2 * (size_t)(out * mc.ldt));
+    mc.dDb = reinterpret_cast<__half*>(q); q += al(2 * (size_t)wn);
     mc.G = reinterpret_cast<float*>(q);
   }
   return true;
@@ -498,12 +498,12 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   if (!mat_prepare(c, w, ad, p, g, S, bwd, mc, err)) return 1;
   MatTarget& t = mc.t;
   if (mat_target_build(c, t, nullptr, err)) return 1;
-  if (k_cvt_bf16(c, x, S * in, mc.xb, err)) return 1;
+  if (k_cvt_f16(c, x, S * in, mc.xb, err)) return 1;
   if (y) {
     GemmDesc d;   // y = x W_eff^T + bias
     d.M = (int)S; d.N = (int)out; d.K = (int)in;
     d.a = mc.xb; d.lda = in;
-    d.bsrc = kB_BF16_KMAJOR; d.b = t.wb; d.ldb = in;
+    d.bsrc = kB_F16_KMAJOR; d.b = t.wb; d.ldb = in;
     d.col_bias = bias;
     d.out = y; d.ldo = out;
     d.name = "mat.fwd";
@@ -517,12 +517,12 @@ int mat_run(Ctx* c, const Weight* w, const sa3k_mat_adapter* ad, const MatPlan& 
   if (!zero(t.dA, (int64_t)r * in) || !zero(t.dB, out * r) || !zero(t.dM, (int64_t)r * r) || !zero(t.dmr, out) ||
       !zero(t.dmc, in))
     return check_launch("memset", err);
-  if (k_cvt_bf16(c, dy, S * out, mc.dyb, err)) return 1;
+  if (k_cvt_f16(c, dy, S * out, mc.dyb, err)) return 1;
   if (dx) {
     GemmDesc d;   // dx = dy W_eff
     d.M = (int)S; d.N = (int)in; d.K = (int)out;
     d.a = mc.dyb; d.lda = out;
-    d.bsrc = kB_BF16_MNMAJOR; d.b = t.wb; d.ldb = in;
+    d.bsrc = kB_F16_MNMAJOR; d.b = t.wb; d.ldb = in;
     d.out = dx; d.ldo = in;
     d.name = "mat.dx";
     if (gemm(c, d, err)) return 1;
@@ -553,7 +553,7 @@ void mat_target_bind(MatTarget& t, void* mem) {
   auto take = [&](size_t bytes) { uint8_t* q = p; p += al(bytes); return q; };
   const size_t wn = (size_t)(t.in * t.out);
   t.V = reinterpret_cast<float*>(take(4 * wn));
-  t.wb = reinterpret_cast<__nv_bfloat16*>(take(2 * wn));
+  t.wb = reinterpret_cast<__half*>(take(2 * wn));
   t.P = reinterpret_cast<float*>(take(4 * (size_t)t.out * t.rank));
   t.PG = reinterpret_cast<float*>(take(4 * (size_t)t.out * t.rank));
   t.Q = reinterpret_cast<float*>(take(4 * (size_t)t.rank * t.in));
@@ -563,8 +563,8 @@ void mat_target_bind(MatTarget& t, void* mem) {
   t.rn2 = reinterpret_cast<double*>(take(8 * t.out));
   t.csq = reinterpret_cast<double*>(take(8 * t.in));
   t.tc = reinterpret_cast<double*>(take(8 * t.in));
-  t.Qb = reinterpret_cast<__nv_bfloat16*>(take(2 * (size_t)t.rank * t.in));
-  t.Btb = reinterpret_cast<__nv_bfloat16*>(take(2 * (size_t)t.rank * t.out));
+  t.Qb = reinterpret_cast<__half*>(take(2 * (size_t)t.rank * t.in));
+  t.Btb = reinterpret_cast<__half*>(take(2 * (size_t)t.rank * t.out));
 }
 
 int mat_target_build(Ctx* c, MatTarget& t, float* weff_f32, std::string& err) {
@@ -609,8 +609,8 @@ int mat_target_build(Ctx* c, MatTarget& t, float* weff_f32, std::string& err) {
   return check_launch("mat pack", err);
 }
 
-int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M, const __nv_bfloat16* x,
-                        float* G, __nv_bfloat16* dzt, int64_t ldt, __nv_bfloat16* dDb, std::string& err) {
+int mat_target_backward(Ctx* c, MatTarget& t, const __half* dz, int64_t M, const __half* x,
+                        float* G, __half* dzt, int64_t ldt, __half* dDb, std::string& err) {
   const int64_t in = t.in, out = t.out;
   const int r = t.rank;
   const cudaStream_t st = c->stream;
@@ -620,7 +620,7 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   }
   {
     ProfScope prof_(c, "mat.transpose");
-    transpose_bf16_bf16_kernel<<<dim3((unsigned)((M + 63) / 64), (unsigned)((out + 63) / 64)), dim3(32, 8), 0, st>>>(
+    transpose_f16_kernel<<<dim3((unsigned)((M + 63) / 64), (unsigned)((out + 63) / 64)), dim3(32, 8), 0, st>>>(
         dz, M, out, dzt, ldt);
     if (check_launch("mat transpose", err)) return 1;
   }
@@ -628,7 +628,7 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
     GemmDesc d;   // G = dz^T x  [out][in], K = token rows
     d.M = (int)out; d.N = (int)in; d.K = (int)M;
     d.a = dzt; d.lda = ldt;
-    d.bsrc = kB_BF16_MNMAJOR; d.b = x; d.ldb = in;
+    d.bsrc = kB_F16_MNMAJOR; d.b = x; d.ldb = in;
     d.out = G; d.ldo = in;
     d.name = "mat.dW";
     if (gemm(c, d, err)) return 1;
@@ -655,7 +655,7 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
     GemmDesc d;   // dB += dD A^T, or PG = dD V (-xs)  [out][r], K = in
     d.M = (int)out; d.N = r; d.K = (int)in;
     d.a = dDb; d.lda = in;
-    d.bsrc = kB_BF16_KMAJOR; d.b = t.Qb; d.ldb = in;
+    d.bsrc = kB_F16_KMAJOR; d.b = t.Qb; d.ldb = in;
     d.out = t.xs ? t.PG : t.dB; d.ldo = r; d.accumulate = 1; d.bn = 16;
     d.atomic_split = 1;
     d.name = "mat.dB";
@@ -669,7 +669,7 @@ int mat_target_backward(Ctx* c, MatTarget& t, const __nv_bfloat16* dz, int64_t M
   GemmDesc d;   // dA^T += dD^T B  [in][r] (dD read MN-major), stored transposed as dA [r][in]
   d.M = (int)in; d.N = r; d.K = (int)out;
   d.a = dDb; d.lda = in; d.a_mn = 1;
-  d.bsrc = kB_BF16_KMAJOR; d.b = t.Btb; d.ldb = out;
+  d.bsrc = kB_F16_KMAJOR; d.b = t.Btb; d.ldb = out;
   d.out = t.dA; d.ldo = in; d.out_trans = 1; d.accumulate = 1; d.bn = 16;
   d.atomic_split = 1;
   d.name = "mat.dA";

@@ -7,7 +7,7 @@
 //   Q8_0: codes int8 [out][in];         scales f32   [in/32][out] = d
 //   Q4_K: codes u8   [out][in/2] (element 2j in the low nibble of byte j, 2j+1 in the high);
 //         scales float2 [in/32][out] = (d*sc, dmin*m) for each 32-element sub-block.
-//   F16 / F32: bf16 [out][in].
+//   F16 / F32: f16 [out][in].
 // value(o, i) = code * d (Q8_0) or (d*sc) * code - dmin*m (Q4_K) in f32 is exactly what
 // ggml-quants.c computes; dequant_kernel below is the bit-exactness probe for that claim.
 #include "sa3k_internal.h"
@@ -73,14 +73,14 @@ __global__ void repack_q4_k_kernel(const uint8_t* __restrict__ raw, int64_t in, 
   }
 }
 
-__global__ void repack_f16_kernel(const __half* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
+__global__ void repack_f16_kernel(const __half* __restrict__ src, int64_t n, __half* __restrict__ dst) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = __float2bfloat16_rn(__half2float(src[i]));
+    dst[i] = __float2half_rn(__half2float(src[i]));
 }
 
-__global__ void repack_f32_kernel(const float* __restrict__ src, int64_t n, __nv_bfloat16* __restrict__ dst) {
+__global__ void repack_f32_kernel(const float* __restrict__ src, int64_t n, __half* __restrict__ dst) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    dst[i] = __float2bfloat16_rn(src[i]);
+    dst[i] = __float2half_rn(src[i]);
 }
 
 __global__ void dequant_kernel(const Weight w, float* __restrict__ dst) {
@@ -108,16 +108,16 @@ __global__ void row_norms_kernel(const Weight w, float eps, float* __restrict__ 
   }
 }
 
-// bf16 operand copy of a quantized weight: the exact f32 dequantized value, rounded once.
-__global__ void dequant_bf16_kernel(const Weight w, __nv_bfloat16* __restrict__ dst) {
+// f16 operand copy of a quantized weight: the exact f32 dequantized value, rounded once.
+__global__ void dequant_f16_kernel(const Weight w, __half* __restrict__ dst) {
   const int64_t n = w.in * w.out;
   for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += (int64_t)gridDim.x * blockDim.x)
-    dst[k] = __float2bfloat16_rn(wval(w, k / w.in, k % w.in));
+    dst[k] = __float2half_rn(wval(w, k / w.in, k % w.in));
 }
 
-int weight_cache_bf16(Ctx* c, Weight* w, std::string& err) {
+int weight_cache_f16(Ctx* c, Weight* w, std::string& err) {
   ProfScope prof_(c, "weight cache");
-  dequant_bf16_kernel<<<1184, 256, 0, c->stream>>>(*w, w->bf16);
+  dequant_f16_kernel<<<1184, 256, 0, c->stream>>>(*w, w->f16);
   return check_launch("weight cache", err);
 }
 
@@ -136,9 +136,9 @@ int weight_repack(Ctx* c, Weight* w, std::string& err) {
         reinterpret_cast<const uint8_t*>(w->raw), w->in, w->out,
         reinterpret_cast<uint8_t*>(w->codes), reinterpret_cast<float2*>(w->scales));
   } else if (w->type == kTypeF16) {
-    repack_f16_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<const __half*>(w->raw), w->in * w->out, w->bf16);
+    repack_f16_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<const __half*>(w->raw), w->in * w->out, w->f16);
   } else {
-    repack_f32_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<const float*>(w->raw), w->in * w->out, w->bf16);
+    repack_f32_kernel<<<1184, 256, 0, st>>>(reinterpret_cast<const float*>(w->raw), w->in * w->out, w->f16);
   }
   return check_launch("weight repack", err);
 }

@@ -7,7 +7,6 @@
 #pragma once
 
 #include <cuda.h>
-#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -233,8 +232,8 @@ struct WaiterW {
   }
 };
 
-// D(tmem) (+)= A(smem desc) * B(smem desc), bf16 in, f32 accumulate.
-__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+// D(tmem) (+)= A(smem desc) * B(smem desc), f16 in, f32 accumulate.
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
@@ -246,7 +245,7 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint6
 
 // Warp-wide forms: every lane of the warp executes them with warp-uniform operands (so the
 // operands can stay in uniform registers) and one elected lane issues the instruction.
-__device__ __forceinline__ void umma_bf16_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+__device__ __forceinline__ void umma_f16_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                             uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p, e;\n\t"
@@ -257,7 +256,7 @@ __device__ __forceinline__ void umma_bf16_w(uint32_t d_tmem, uint64_t adesc, uin
       : "memory");
 }
 
-// D (tmem) (+)= A (tmem, bf16 packed two per 32-bit column) * B (smem descriptor), warp-wide.
+// D (tmem) (+)= A (tmem, f16 packed two per 32-bit column) * B (smem descriptor), warp-wide.
 __device__ __forceinline__ void umma_ts_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accumulate) {
   asm volatile(
@@ -333,11 +332,10 @@ __device__ __forceinline__ uint64_t make_sdesc(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B and an f32 accumulator.
-__host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn, int b_mn) {
+// Instruction descriptor for kind::f16 with IEEE half A/B (format 0 in bits 7-9 and 10-12) and an
+// f32 accumulator.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int a_mn, int b_mn) {
   return (1u << 4)                       // D format f32
-         | (1u << 7)                     // A bf16
-         | (1u << 10)                    // B bf16
          | ((uint32_t)a_mn << 15)        // A major (0 = K, 1 = MN)
          | ((uint32_t)b_mn << 16)        // B major
          | ((uint32_t)(N >> 3) << 17)    // N / 8
@@ -369,8 +367,8 @@ __device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
   return d;
 }
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 

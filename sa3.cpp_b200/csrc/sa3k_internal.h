@@ -2,7 +2,6 @@
 #pragma once
 
 #include <cuda.h>
-#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -25,7 +24,7 @@ struct Weight {
   void* raw = nullptr;               // F16/F32: the original values (dequant probe, row norms)
   int8_t* codes = nullptr;           // Q8_0 int8 [out][in] | Q4_K nibble pairs [out][in/2]
   float* scales = nullptr;           // Q8_0 f32 [in/32][out] | Q4_K float2 [in/32][out]
-  __nv_bfloat16* bf16 = nullptr;     // bf16 [out][in] operand copy (F16/F32 always; Q8_0/Q4_K
+  __half* f16 = nullptr;     // f16 [out][in] operand copy (F16/F32 always; Q8_0/Q4_K
                                      // when the context keeps a dequantized cache)
   int device = 0;
 };
@@ -55,7 +54,7 @@ struct Ctx {
   size_t sm_count = 148;
   bool timing = false;
   bool timing_graph = false;         // timing events live in a captured CUDA graph
-  bool weight_cache = true;          // quantized weights keep a dequantized bf16 operand copy
+  bool weight_cache = true;          // quantized weights keep a dequantized f16 operand copy
   bool smem_dequant = false;         // force the in-smem dequant GEMM path for quantized weights
   int tile_n = 0;                    // main-GEMM N tile: 0 = cost model, 128 or 256 = fixed
   int gemm_pair = 1;                 // CTA-pair (cta_group::2) GEMMs: 0 never, 1 where they pay, 2 always
@@ -138,35 +137,35 @@ enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61, kSlotSplitC
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
 
 int weight_repack(Ctx* c, Weight* w, std::string& err);
-int weight_cache_bf16(Ctx* c, Weight* w, std::string& err);
+int weight_cache_f16(Ctx* c, Weight* w, std::string& err);
 int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err);
 int weight_row_norms(Ctx* c, const Weight* w, float eps, float* nsq, float* nrm, std::string& err);
 
 // ----------------------------------------------------------------------------- GEMM engine
 // B operand sources.
 enum BSource : int {
-  kB_BF16_KMAJOR = 0,   // bf16 [N][K]
-  kB_BF16_MNMAJOR = 1,  // bf16 [K][N]
+  kB_F16_KMAJOR = 0,   // f16 [N][K]
+  kB_F16_MNMAJOR = 1,  // f16 [K][N]
   kB_WEIGHT_NT = 2,     // weight W[out = N][in = K]           (y = x W^T)
   kB_WEIGHT_TN = 3,     // weight W[out = K][in = N], used as W^T (dx = dy W)
 };
 
 struct GemmDesc {
   int M = 0, N = 0, K = 0;
-  // A: bf16, K-major [M][lda] or (a_mn) MN-major [K][lda]
-  const __nv_bfloat16* a = nullptr;
+  // A: f16, K-major [M][lda] or (a_mn) MN-major [K][lda]
+  const __half* a = nullptr;
   long lda = 0;
   int a_mn = 0;
   // B
-  int bsrc = kB_BF16_KMAJOR;
-  const __nv_bfloat16* b = nullptr;
+  int bsrc = kB_F16_KMAJOR;
+  const __half* b = nullptr;
   long ldb = 0;
   const Weight* w = nullptr;
-  // K = 16 extension: ext_at bf16 [16][ld_ext] (the rank-16 left factor transposed, read
-  // MN-major), ext_b bf16 [N][64] (columns 16..63 are not read)
-  const __nv_bfloat16* ext_at = nullptr;
+  // K = 16 extension: ext_at f16 [16][ld_ext] (the rank-16 left factor transposed, read
+  // MN-major), ext_b f16 [N][64] (columns 16..63 are not read)
+  const __half* ext_at = nullptr;
   long ld_ext = 0;
-  const __nv_bfloat16* ext_b = nullptr;
+  const __half* ext_b = nullptr;
   // epilogue
   const float* col_scale = nullptr;
   const float* col_bias = nullptr;
@@ -175,12 +174,12 @@ struct GemmDesc {
   long ldo = 0;
   int out_trans = 0;
   int accumulate = 0;
-  __nv_bfloat16* out_bf = nullptr;    // bf_scale * the f32 value, row-major or (out_bf_trans) transposed
-  long ldo_bf = 0;
-  int out_bf_trans = 0;
-  float bf_scale = 1.0f;
-  __nv_bfloat16* out_bf_t = nullptr;  // the unscaled value again as bf16, transposed [N][ldo_bf_t]
-  long ldo_bf_t = 0;
+  __half* out_h = nullptr;    // h_scale * the f32 value, row-major or (out_h_trans) transposed
+  long ldo_h = 0;
+  int out_h_trans = 0;
+  float h_scale = 1.0f;
+  __half* out_h_t = nullptr;  // the unscaled value again as f16, transposed [N][ldo_h_t]
+  long ldo_h_t = 0;
   int bn = 128;         // N tile (16, 128)
   // split-K partial sums may be added into `out` with f32 atomics (no reduction pass; the
   // summation order, and so the last bits, vary from run to run).  f32 `out` only.

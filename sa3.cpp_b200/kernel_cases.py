@@ -83,14 +83,14 @@ def gemm_case(a):
 
 def attention_case(a):
     """Self-attention of the DiT step: B x H heads of Sq = Sk tokens, head_dim 64, q / k / v /
-    o as [B][S][H * 64] bf16 (the layout of the fused projection), forward and backward."""
+    o as [B][S][H * 64] f16 (the layout of the fused projection), forward and backward."""
     import torch
     import sa3k
     torch.cuda.set_device(0)
     ctx = sa3k.Context(0)
     g = torch.Generator(device="cuda").manual_seed(0)
     B, H, S = a.b, a.h, a.s
-    bf = lambda: torch.randn(B, S, H * 64, generator=g, device="cuda").to(torch.bfloat16)
+    bf = lambda: torch.randn(B, S, H * 64, generator=g, device="cuda").to(torch.float16)
     q, k, v, dO = bf(), bf(), bf(), bf()
     o = torch.empty_like(q)
     dq, dk, dv = (torch.empty(B, S, H * 64, device="cuda") for _ in range(3))

@@ -32,7 +32,7 @@ ABI_SYMBOLS = (
     "sa3k_lora_chain_info", "sa3k_linear_fwd_chain", "sa3k_mat_effective_weight", "sa3k_linear_mat_fwd",
     "sa3k_linear_mat_fwd_bwd", "sa3k_dit_adapter_layout", "sa3k_dit_set_xs_bases",
 )
-OPT_WEIGHT_BF16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
+OPT_WEIGHT_F16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
 
 

@@ -2,8 +2,8 @@
 RMSNorm + partial NeoX RoPE head preparation (src/dit.h:195, 209-217; src/nn.h:53-59), forward and
 backward, through the C ABI, against float64 torch autograd over the oracle's restatement.
 
-Inputs are rounded to bf16 first (the kernels' operand type), so the comparison isolates the
-kernels' own error; tolerance rel-L2 <= 1e-2 (bf16 operands, f32 accumulation)."""
+Inputs are rounded to f16 (IEEE half) first (the kernels' operand type), so the comparison isolates the
+kernels' own error; tolerance rel-L2 <= 1e-2 (16-bit operands, f32 accumulation)."""
 import math
 
 import numpy as np
@@ -51,7 +51,7 @@ def test_attention_fwd_bwd(ctx, B, H, Sq, Sk, window, token_major):
     import torch
     import sa3k
     g = torch.Generator().manual_seed(B * 1000 + Sq)
-    bf = lambda *s: torch.randn(*s, generator=g).to(torch.bfloat16)
+    bf = lambda *s: torch.randn(*s, generator=g).to(torch.float16)
     q, k, v, dO = bf(B, H, Sq, 64), bf(B, H, Sk, 64), bf(B, H, Sk, 64), bf(B, H, Sq, 64)
     scale = 1.0 / math.sqrt(64)
     ro, rdq, rdk, rdv = _ref_attention(q.double(), k.double(), v.double(), dO.double(), scale,
@@ -89,7 +89,7 @@ def test_attention_dq_only_for_frozen_context(ctx):
     import sa3k
     B, H, Sq, Sk = 1, 2, 130, 128
     g = torch.Generator().manual_seed(5)
-    q, k, v, dO = (torch.randn(B, H, s, 64, generator=g).to(torch.bfloat16) for s in (Sq, Sk, Sk, Sq))
+    q, k, v, dO = (torch.randn(B, H, s, 64, generator=g).to(torch.float16) for s in (Sq, Sk, Sk, Sq))
     _, rdq, _, _ = _ref_attention(q.double(), k.double(), v.double(), dO.double(), 0.125, None)
     qs, ks = (H * Sq * 64, Sq * 64, 64), (H * Sk * 64, Sk * 64, 64)
     qd, kd, vd, dod = q.cuda(), k.cuda(), v.cuda(), dO.cuda()
@@ -132,7 +132,7 @@ def test_head_prep_norm_rope_fwd_bwd(ctx, rot):
     ref.backward(up)
 
     yd = y.float().cuda()
-    out = torch.empty(T, ncols, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(T, ncols, dtype=torch.float16, device="cuda")
     rq = torch.empty(T, H, device="cuda")
     rk = torch.empty(T, H, device="cuda")
     gqd, gkd = gq.float().cuda(), gk.float().cuda()
@@ -150,24 +150,24 @@ def test_head_prep_norm_rope_fwd_bwd(ctx, rot):
 
 def test_config3_banded_rope_attention(ctx):
     """batch 2, 24 heads, head_dim 64, 2048 frames, window +-256, NeoX RoPE on
-    q and k (rot 32, base 1e4), bf16 N(0,1) inputs.  The full problem runs on the GPU; two heads
+    q and k (rot 32, base 1e4), f16 N(0,1) inputs.  The full problem runs on the GPU; two heads
     are checked against float64 autograd (the oracle cost grows with S^2)."""
     import torch
     import sa3k
     B, H, S, W = 2, 24, 2048, 256
     dim = H * 64
     g = torch.Generator().manual_seed(3)
-    qkv = torch.randn(B * S, 3 * dim, generator=g).to(torch.bfloat16).float()
-    dO = torch.randn(B, S, dim, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(B * S, 3 * dim, generator=g).to(torch.float16).float()
+    dO = torch.randn(B, S, dim, generator=g).to(torch.float16)
     yd = qkv.cuda()
-    prep = torch.empty(B * S, 3 * dim, dtype=torch.bfloat16, device="cuda")
+    prep = torch.empty(B * S, 3 * dim, dtype=torch.float16, device="cuda")
     sl = [sa3k.HeadSliceC(0, None, 1, None), sa3k.HeadSliceC(dim, None, 1, None), sa3k.HeadSliceC(2 * dim, None, 0, None)]
     ctx.head_prep_fwd(yd, B * S, 3 * dim, H, sl, S, 1e-6, 32, 10000.0, prep)
     T4 = sa3k.t4
     st = (S * 3 * dim, 64, 3 * dim)
     so = (S * dim, 64, dim)
     q, k, v = prep, prep[:, dim:], prep[:, 2 * dim:]
-    o = torch.empty(B * S, dim, dtype=torch.bfloat16, device="cuda")
+    o = torch.empty(B * S, dim, dtype=torch.float16, device="cuda")
     lse = torch.empty(B * H * S, device="cuda")
     ctx.attention_fwd(B, H, S, S, 0.125, W, T4(q, *st), T4(k, *st), T4(v, *st), T4(o, *so), lse)
     d3 = torch.zeros(B * S, 3 * dim, device="cuda")
@@ -187,10 +187,10 @@ def test_config3_banded_rope_attention(ctx):
     kh = torch.stack([oracle.rope_neox(x[b, :, 1], pos, 32, 10000.0) for b in range(B)])
     vh = x[:, :, 2]
     tr = lambda t: t.permute(0, 2, 1, 3)
-    # the kernel consumes the bf16-rounded roped q / k; round the reference the same way
+    # the kernel consumes the f16-rounded roped q / k; round the reference the same way
     # (straight-through: the rounded value forward, the identity backward)
-    qr = tr(qh).detach().to(torch.bfloat16).double() + (tr(qh) - tr(qh).detach())
-    kr = tr(kh).detach().to(torch.bfloat16).double() + (tr(kh) - tr(kh).detach())
+    qr = tr(qh).detach().to(torch.float16).double() + (tr(qh) - tr(qh).detach())
+    kr = tr(kh).detach().to(torch.float16).double() + (tr(kh) - tr(kh).detach())
     ref_o = oracle.sdpa(qr, kr, tr(vh), 0.125, W)
     dOr = dO.double().reshape(B, S, H, 64)[:, :, heads].permute(0, 2, 1, 3)
     ref_o.backward(dOr)

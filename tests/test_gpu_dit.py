@@ -108,7 +108,7 @@ def _reference(cfg, deq, ad, inputs):
     sum(losses).backward()
     # (adapters the loss does not reach, the local.* ones without a local input, get no gradient)
     grads = {n: tuple(np.zeros(t.shape) if t.grad is None else t.grad.numpy() for t in v) for n, v in leaves.items()}
-    return np.array([float(l) for l in losses]), grads
+    return np.array([float(l.detach()) for l in losses]), grads
 
 
 # (differential, scope, adapter): the benchmark's four per-block targets, and the reference's
@@ -136,7 +136,7 @@ def test_dit_step_matches_oracle(ctx, differential, scope, adapter, local_dim):
     loss = np.zeros(B, np.float32)
     dit.forward_backward(B, T, CTX, *inputs, loss=loss)
     ctx.sync()
-    assert np.max(np.abs(loss - ref_loss) / ref_loss) < 1e-2, (loss, ref_loss)
+    assert np.max(np.abs(loss - ref_loss) / ref_loss) < 1e-3, (loss, ref_loss)
     grads = np.zeros(dit.size(), np.float32)
     dit.copy(1, grads, to_model=False)
     worst = {}
@@ -153,16 +153,11 @@ def test_dit_step_matches_oracle(ctx, differential, scope, adapter, local_dim):
             continue
         for lab, g, r in zip(("dA", "dB", "dm"), got, ref):
             worst[f"{name}:{lab}"] = rel_l2(g, r)
-    # bf16 operands through the whole step: the typical entry (median) within 1.5e-2, each single
-    # entry within 3e-2.  Measured medians: 0.5e-2 .. 0.9e-2 with standard attention, 1.05e-2 with
-    # differential attention (its two softmax streams are close at random init, and each is
-    # rounded to bf16 before the difference).  Single entries depend on the inputs'
-    # conditioning: block 0's cross.out dA of the core / lora case measured 2.4e-2, 1.3e-2 and
-    # 0.7e-2 on seeds 0, 1, 2.
+    # the north star's bar for 16-bit operands, per tensor: every adapter gradient within rel-L2
+    # 1e-2 of the float64 reference
     top = sorted(((v, k) for k, v in worst.items()), reverse=True)[:6]
     print(f"[{differential} {scope} {adapter}] worst:", "; ".join(f"{k} {v:.3g}" for v, k in top))
-    assert np.median(list(worst.values())) < 1.5e-2, top
-    bad = sorted((v, k) for k, v in worst.items() if not v < 3e-2)
+    bad = sorted((v, k) for k, v in worst.items() if not v < 1e-2)
     assert not bad, "; ".join(f"{k} {v:.3g}" for v, k in bad)
 
     # one averaged (count = B) + clipped AdamW update on the flat state

@@ -3,7 +3,7 @@ bora, the -xs forms; src/train_dit.h:90-164: W_eff = train_lora_effective_weight
 target's weight) against float64 torch autograd through the oracle's dit_loss.  The same small
 Q8_0 DiT as tests/test_gpu_dit.py; checked: per-sample loss, the device magnitude init (row and
 column norms of the dequantized base, src/train_lora.h:141-190) and every adapter gradient, with
-the same tolerance as the functional step (median rel-L2 < 1.5e-2, each < 3e-2)."""
+the same tolerance as the functional step (every tensor within rel-L2 1e-2)."""
 import math
 
 import numpy as np
@@ -141,7 +141,7 @@ def test_dit_step_materialized_matches_oracle(ctx, adapter_type, scope, differen
     loss = np.zeros(B, np.float32)
     dit.forward_backward(B, T, CTX, *inputs, loss=loss)
     ctx.sync()
-    assert np.max(np.abs(loss - ref_loss) / ref_loss) < 1e-2, (loss, ref_loss)
+    assert np.max(np.abs(loss - ref_loss) / ref_loss) < 1e-3, (loss, ref_loss)
     grads = np.zeros(dit.size(), np.float32)
     dit.copy(1, grads, to_model=False)
     worst = {}
@@ -154,8 +154,8 @@ def test_dit_step_materialized_matches_oracle(ctx, adapter_type, scope, differen
             worst[f"{name}:d{key}"] = rel_l2(grads[off:off + r.size].reshape(r.shape), r)
     top = sorted(((v, k) for k, v in worst.items()), reverse=True)[:6]
     print(f"[{adapter_type} {scope} {differential}] worst:", "; ".join(f"{k} {v:.3g}" for v, k in top))
-    assert np.median(list(worst.values())) < 1.5e-2, top
-    bad = sorted((v, k) for k, v in worst.items() if not v < 3e-2)
+    # the north star's bar for 16-bit operands, per tensor
+    bad = sorted((v, k) for k, v in worst.items() if not v < 1e-2)
     assert not bad, "; ".join(f"{k} {v:.3g}" for v, k in bad)
 
 

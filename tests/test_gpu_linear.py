@@ -2,7 +2,7 @@
 
 Dequantization is checked bit for bit against the C oracle (which is pinned to gguf-py);
 forward outputs and every gradient are checked against the float64 oracle on the same
-dequantized weights with the north star's bf16-operand tolerance, rel-L2 <= 1e-2.
+dequantized weights with the north star's 16-bit-operand tolerance, rel-L2 <= 1e-2.
 """
 import numpy as np
 import pytest
@@ -10,7 +10,7 @@ import pytest
 import oracle
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-2      # rel-L2, bf16 tensor-core operands with f32 accumulation
+TOL = 1e-2      # rel-L2, 16-bit tensor-core operands with f32 accumulation
 
 
 def rel_l2(a, b):
@@ -79,7 +79,7 @@ def test_row_norms(ctx, qtype):
     np.testing.assert_allclose(nrm.cpu().numpy(), ref_nrm, rtol=1e-6)
 
 
-@pytest.fixture(params=["bf16_cache", "smem_dequant"])
+@pytest.fixture(params=["f16_cache", "smem_dequant"])
 def operand_path(request, ctx):
     """Run a test through both operand paths of the quantized GEMMs (identical numerics)."""
     import sa3k
@@ -262,7 +262,7 @@ def test_bad_arguments_raise(ctx):
 
 
 def test_smem_and_cache_paths_agree_bitwise(ctx):
-    """Both operand paths round the same exact f32 dequantized value once to bf16 and run the same
+    """Both operand paths round the same exact f32 dequantized value once to f16 and run the same
     MMA sequence, so their forward outputs match bit for bit."""
     import torch
     import sa3k

@@ -60,7 +60,7 @@ def test_contexts_on_two_devices(attn_tc):
     A = rng.normal(0, 1 / math.sqrt(IN), (R, IN)).astype(np.float32)
     Bm = rng.normal(0, 0.01, (OUT, R)).astype(np.float32)
     g = torch.Generator().manual_seed(4)
-    q, k, v, dO = (torch.randn(2, 3, 300, 64, generator=g).to(torch.bfloat16) for _ in range(4))
+    q, k, v, dO = (torch.randn(2, 3, 300, 64, generator=g).to(torch.float16) for _ in range(4))
     r0 = _run(0, raw, IN, OUT, x, dy, A, Bm, q, k, v, dO, attn_tc)
     r1 = _run(1, raw, IN, OUT, x, dy, A, Bm, q, k, v, dO, attn_tc)
     for name, a, b in zip(("y", "dx", "dA", "dB", "o", "dq", "dk", "dv"), r0, r1):

@@ -14,7 +14,7 @@ def _inputs(B, H, Sq, Sk, seed):
     import torch
     g = torch.Generator(device="cuda").manual_seed(seed)
     # token-major [B][S][H][64], the layout of the DiT's fused projection outputs
-    bf = lambda S: torch.randn(B, S, H, 64, generator=g, device="cuda").to(torch.bfloat16)
+    bf = lambda S: torch.randn(B, S, H, 64, generator=g, device="cuda").to(torch.float16)
     return bf(Sq), bf(Sk), bf(Sk), bf(Sq)
 
 
@@ -56,7 +56,7 @@ def test_noalloc_rejects_sizes_beyond_its_scratch(ctx):
     import sa3k
     # 2**20 + 64 query rows: refused on the host before anything is launched
     B, H, Sq = 1, 1, (1 << 20) + 64
-    t = torch.empty(1, dtype=torch.bfloat16, device="cuda")
+    t = torch.empty(1, dtype=torch.float16, device="cuda")
     f = torch.empty(1, device="cuda")
     T4 = sa3k.t4
     with pytest.raises(sa3k.Sa3kError, match="exceeds its fixed scratch"):
