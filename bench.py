@@ -21,6 +21,7 @@ import json
 import os
 import statistics
 import subprocess
+import tempfile
 import sys
 import time
 
@@ -61,10 +62,10 @@ class Clocks:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(REPO, "gpurun_out", f"clocks_{index}.csv")
+        fd, self.path = tempfile.mkstemp(prefix=f"sa3k_clocks_{index}_", suffix=".csv")
+        os.close(fd)
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), "--query-gpu=clocks.sm,clocks.max.sm,power.draw,"

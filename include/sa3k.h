@@ -134,6 +134,10 @@ int sa3k_dequant(sa3k_ctx* ctx, const sa3k_weight* w, float* dst, char* err, int
 int sa3k_row_norms(sa3k_ctx* ctx, const sa3k_weight* w, float eps, float* base_norm_sq,
                    float* norm, char* err, int err_len);
 
+/* Per input column: norm[i] = sqrt(sum_o W[o][i]^2), f64 accumulation.  Replaces train_col_norms
+ * (src/train_lora.h:176-190), the magnitude init of dora-cols and bora's column magnitude. */
+int sa3k_col_norms(sa3k_ctx* ctx, const sa3k_weight* w, float* norm, char* err, int err_len);
+
 /* One functional adapter on a linear, as DitLoraParam (src/dit.h:65-88). rank <= 16. */
 typedef struct sa3k_adapter {
   const float* A;             /* [rank][in]                                   */

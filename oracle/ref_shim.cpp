@@ -5,7 +5,7 @@
 // oracle/_ref/libsa3ref.so, is the reference's own CPU code for:
 //   - AdamW:        src/train_optimizer.h:42-65   (sa3::adamw_update_vector)
 //   - LR schedule:  src/train_optimizer.h:20-26   (sa3::inverse_lr)
-//   - diffusion:    src/train_diffusion.h:62-78   (sa3::TrainDiffusionSampler::sample_at)
+//   - diffusion:    src/train_diffusion.h:50-125  (sa3::TrainDiffusionSampler: sample_at, draw_t)
 // The average / global-norm clip of src/train_loop.h:147-171 sits in a header that pulls in
 // ggml, so it cannot be compiled here; tests pin it through the oracle restatement instead.
 #include "train_diffusion.h"
@@ -62,6 +62,22 @@ int sa3ref_diffusion_sample_at(unsigned long long seed, const float* z, long n, 
     std::memcpy(noise, out.noise.data(), sizeof(float) * (size_t)n);
     std::memcpy(x_t, out.x_t.data(), sizeof(float) * (size_t)n);
     std::memcpy(v_target, out.velocity_target.data(), sizeof(float) * (size_t)n);
+    return 0;
+}
+
+// n_steps draws of one sampler stream: t_out[i] = draw_t(), then sample_at(z, t) fills
+// noise[i*n ...]: the interleaving of the trainer's loop (draw_t, then the noise of that sample).
+int sa3ref_diffusion_stream(unsigned long long seed, const char* mode, const float* z, long n, int n_steps,
+                            float* t_out, float* noise) {
+    sa3::TrainDiffusionSampler s(seed, mode);
+    std::vector<float> zz(z, z + n);
+    sa3::TrainDiffusionSample out;
+    std::string e;
+    for (int i = 0; i < n_steps; ++i) {
+        t_out[i] = s.draw_t();
+        if (!s.sample_at(zz, t_out[i], out, e)) return 1;
+        std::memcpy(noise + (size_t)i * n, out.noise.data(), sizeof(float) * (size_t)n);
+    }
     return 0;
 }
 

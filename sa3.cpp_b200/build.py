@@ -20,14 +20,14 @@ NVCC = os.environ.get("NVCC", "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
          "-I", os.path.join(os.path.dirname(HERE), "include")]
-SOURCES = ["quant.cu", "gemm_tc.cu", "gemm_r16.cu", "lora.cu", "adamw.cu", "attention.cu", "attention_tc.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu", "dp.cu", "gguf_io.cu", "checkpoint.cu", "lora_chain.cu", "materialize.cu"]
+SOURCES = ["quant.cu", "gemm_tc.cu", "gemm_r16.cu", "lora.cu", "adamw.cu", "attention.cu", "attention_tc.cu", "dit_ops.cu", "linear.cu", "dit.cu", "api.cu", "dp.cu", "gguf_io.cu", "checkpoint.cu", "lora_chain.cu", "materialize.cu", "sa3_train.cpp"]
 
 
 def _compile(src, verbose):
-    obj = os.path.join(OBJ, src.replace(".cu", ".o"))
+    obj = os.path.join(OBJ, os.path.splitext(src)[0] + ".o")
     path = os.path.join(CSRC, src)
     deps = [path] + [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
-    deps.append(os.path.join(os.path.dirname(HERE), "include", "sa3k.h"))
+    deps += [os.path.join(os.path.dirname(HERE), "include", h) for h in ("sa3k.h", "sa3_train.h")]
     if os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(d) for d in deps):
         return obj, ""
     cmd = [NVCC, *ARCH, *FLAGS, "-c", path, "-o", obj]

@@ -5,6 +5,7 @@
 #include "linear.h"
 #include "lora_kernels.h"
 #include "sa3k_internal.h"
+#include "materialize.h"
 
 #include <cmath>
 #include <cstdio>
@@ -400,6 +401,14 @@ int sa3k_row_norms(sa3k_ctx* ctx, const sa3k_weight* w, float eps, float* nsq, f
   return 0;
 }
 
+int sa3k_col_norms(sa3k_ctx* ctx, const sa3k_weight* w, float* nrm, char* err, int err_len) {
+  if (!ctx || !w || !nrm) return fill_err(err, err_len, "NULL argument");
+  cudaSetDevice(ctx->c.device);
+  std::string e;
+  if (mat_col_norms(&ctx->c, &w->w, nrm, e)) return fill_err(err, err_len, e);
+  return 0;
+}
+
 int sa3k_linear_fwd(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_adapter* ad, const float* bias,
                     const float* x, int64_t S, float* y, char* err, int err_len) {
   if (!ctx || !w || !x || !y) return fill_err(err, err_len, "NULL argument");
@@ -437,6 +446,10 @@ int sa3k_linear_fwd_bwd_host(sa3k_ctx* ctx, const sa3k_weight* w, const sa3k_ada
                              const float* x_h, const float* dy_h, int64_t S, float* y_h, float* dx_h, float* dA_h,
                              float* dB_h, float* dm_h, char* err, int err_len) {
   if (!ctx || !w || !x_h || !dy_h || !y_h) return fill_err(err, err_len, "NULL argument");
+  // the adapter is validated before its host arrays are read (their sizes follow from the rank)
+  if (adh && (adh->rank < 1 || adh->rank > 16 || !adh->A || !adh->B))
+    return fill_err(err, err_len, "adapter rank must be 1..16 with A and B");
+  if (S <= 0) return fill_err(err, err_len, "S must be positive");
   Ctx* c = &ctx->c;
   cudaSetDevice(c->device);
   const int64_t in = w->w.in, out = w->w.out;

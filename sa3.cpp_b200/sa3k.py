@@ -18,7 +18,7 @@ TYPE_IDS = {"f32": 0, "f16": 1, "q8_0": 8, "q4_k": 12}
 # every symbol include/sa3k.h declares
 ABI_SYMBOLS = (
     "sa3k_version", "sa3k_ctx_create", "sa3k_ctx_destroy", "sa3k_ctx_set_stream", "sa3k_sync",
-    "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_linear_fwd",
+    "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_col_norms", "sa3k_linear_fwd",
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
     "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_attention_bwd_noalloc", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",

@@ -25,7 +25,7 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(REPO, "oracle"))
 import oracle  # noqa: E402
 
-REFERENCE = os.environ.get("SA3_REFERENCE", "/root/reference")
+REFERENCE = os.environ.get("SA3_REFERENCE", "")   # a reference checkout (its tests/ hold the known answers)
 
 
 def gen_q8_0():
@@ -71,6 +71,8 @@ def gen_q4_k():
 
 def quoted_inverse_lr():
     """(step0, lr) pairs quoted in the reference's tests/train_optimizer_test.cpp:35-39."""
+    if not REFERENCE:
+        raise SystemExit("set SA3_REFERENCE to a reference checkout")
     path = os.path.join(REFERENCE, "tests", "train_optimizer_test.cpp")
     txt = open(path).read()
     pairs = re.findall(r"\{\s*(\d+)\s*,\s*([0-9.eE+-]+)f\s*\}", txt)
