@@ -481,74 +481,100 @@ def dit_inputs(cfg, B, seed):
     return [xt, tg, tf, cross, glob]
 
 
-def dit_cpu_block(cfg, seed, reps=1):
-    """Time one block of one sample, forward + backward, of the CPU restatement (torch float32
-    autograd over oracle.dit_block, all host threads); returns seconds per block."""
-    import torch
-    oracle = _oracle()
-    import dit_synth
-    torch.set_num_threads(os.cpu_count())
-    g = torch.Generator().manual_seed(seed)
-    shapes = dit_synth.tensor_shapes(dict(cfg, depth=1))
-    Wd, lora = {}, {}
-    for name, shape in shapes.items():
-        if name.startswith("dit.0."):
-            if dit_synth.is_weight(name):
-                Wd[name] = torch.randn(shape, generator=g) * 0.02
+class DitCpuStep:
+    """The CPU restatement of the config-4 step (float32 torch autograd over oracle.dit_loss, all
+    host threads): every weight of the 24-block model and its DoRA adapters built once, outside
+    any timed region; run(i) is one whole sample -- head, 24 blocks, tail, loss, backward to every
+    adapter -- and returns its seconds."""
+
+    def __init__(self, cfg, seed=7):
+        import torch
+        import dit_synth
+        oracle = _oracle()
+        torch.set_num_threads(os.cpu_count())
+        self.torch, self.oracle, self.cfg = torch, oracle, cfg
+        g = torch.Generator().manual_seed(seed)
+        self.Wd, self.lora = {}, {}
+        shapes = dit_synth.tensor_shapes(cfg)
+        # (every block reads block 0's frozen tensors: the arithmetic, and so the time, is that of
+        # 24 distinct blocks, with a 24x smaller host footprint and set-up)
+        for name, shape in shapes.items():
+            key = ("dit.0." + name.split(".", 2)[2]) if name.split(".")[1].isdigit() else name
+            if key in self.Wd:
+                self.Wd[name] = self.Wd[key]
+            elif dit_synth.is_weight(name):
+                self.Wd[name] = torch.randn(shape, generator=g) * 0.02
+            elif name.endswith("gamma"):
+                self.Wd[name] = torch.ones(shape)
             else:
-                Wd[name] = torch.ones(shape) if name.endswith("gamma") else torch.randn(shape, generator=g) * 0.05
-    for name in dit_synth.default_targets(dict(cfg, depth=1)):
-        out, inn = shapes[name]
-        W = Wd[name]
-        lora[name] = dict(A=(torch.randn(DIT_RANK, inn, generator=g) / inn ** 0.5).requires_grad_(True),
-                          B=(torch.randn(out, DIT_RANK, generator=g) * 0.01).requires_grad_(True),
-                          m=W.norm(dim=1).clone().requires_grad_(True), bns=(W * W).sum(1), scale=1.0)
-    c = oracle.DitCfg(**{k: cfg[k] for k in ("io", "dim", "heads", "cond_dim", "mem_tokens", "rot", "time_dim",
-                                             "ff_inner")}, depth=1)
-    S = cfg["mem_tokens"] + DIT_T
-    x = torch.randn(S, cfg["dim"], generator=g)
-    ctx = torch.randn(DIT_CTX, cfg["dim"], generator=g)
-    gcond = torch.randn(6 * cfg["dim"], generator=g) * 0.1
-    pos = torch.arange(S)
-    times = []
-    for _ in range(reps + 1):
+                self.Wd[name] = torch.randn(shape, generator=g) * 0.05
+        for name in dit_synth.default_targets(cfg):
+            out, inn = shapes[name]
+            W = self.Wd[name]
+            self.lora[name] = dict(A=(torch.randn(DIT_RANK, inn, generator=g) / inn ** 0.5).requires_grad_(True),
+                                   B=(torch.randn(out, DIT_RANK, generator=g) * 0.01).requires_grad_(True),
+                                   m=W.norm(dim=1).clone().requires_grad_(True), bns=(W * W).sum(1),
+                                   scale=DIT_ALPHA / DIT_RANK)
+        self.c = oracle.DitCfg(**{k: cfg[k] for k in ("io", "dim", "depth", "heads", "head_dim", "cond_dim",
+                                                      "mem_tokens", "rot", "time_dim", "ff_inner")}, differential=False)
+        self.inputs = dit_inputs(cfg, 2, seed=seed + 1)
+
+    def run(self, i):
+        torch = self.torch
+        xt, tg, tf, cross, glob = [torch.from_numpy(a[i % 2]) for a in self.inputs]
         t0 = time.perf_counter()
-        y = oracle.dit_block(Wd, lora, "dit.0.", x, ctx, gcond, pos, c)
-        y.sum().backward()
-        times.append(time.perf_counter() - t0)
-    return statistics.median(times[1:]) if reps > 0 else times[0]
+        loss = self.oracle.dit_loss(self.Wd, self.lora, xt, tf, cross, glob, tg, self.c)
+        loss.backward()
+        dt = time.perf_counter() - t0
+        for p in self.lora.values():
+            for k in ("A", "B", "m"):
+                p[k].grad = None
+        return dt
 
 
-def dit_cpu_baseline(cfg):
-    sec = dit_cpu_block(cfg, 7, reps=2)
-    per_sample = sec * cfg["depth"]
-    return {"value": 1.0 / per_sample, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one DiT block of one 1088-token sample, forward + backward, float32 torch CPU restatement "
-                      f"(oracle.dit_block) on {os.cpu_count()} threads, median of 2 = {sec:.2f} s, x {cfg['depth']} "
-                      f"blocks per sample (head / tail < 1% of the FLOPs; ggml, which holds the reference's CPU "
-                      f"kernels, is not available)"}
+def dit_cpu_sample_note(threads):
+    return (f"whole samples of the config-4 step (head, 24 blocks, tail, MSE loss, backward to all 96 DoRA "
+            f"adapters; 1088 tokens, cross 128x768), float32 torch CPU restatement of the reference's math "
+            f"(oracle.dit_loss) on {threads} threads, weights built before timing (the blocks share one block's "
+            f"frozen tensors; adapters per block), the first sample untimed "
+            f"(the reference's own CPU path needs ggml, which is not available)")
+
+
+def dit_cpu_baseline(cfg, n_timed=2):
+    step = DitCpuStep(cfg)
+    step.run(0)
+    sec = statistics.median(step.run(i + 1) for i in range(n_timed))
+    return {"value": 1.0 / sec, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_timed} " + dit_cpu_sample_note(os.cpu_count()) + f"; median {sec:.2f} s per sample"}
+
+
+def dit_config_line(args, cfg):
+    """The workload as both arms name it (the reference arm quotes the same config)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    return {"workload": DIT_WORKLOAD + (f" (depth overridden to {cfg['depth']})" if args.depth else "")
+            + (f" (adapters overridden to {args.adapter_type})" if args.adapter_type != "dora-rows" else ""),
+            "global_batch": DIT_B * world, "seq_len": DIT_T, "parallelism": f"dp{world}",
+            "l2": "256 MB flush between timed steps"}
 
 
 def run_dit_reference(args):
+    """The reference arm: the CPU restatement, each step one whole sample of the workload (a
+    bounded sample: one of the step's 4 samples), after one untimed sample; rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     cfg = dit_cfg()
-    for _ in range(max(1, min(args.warmup, 1))):
-        dit_cpu_block(cfg, 7, reps=0)
-    t0 = time.perf_counter()
-    for i in range(args.steps):
-        dit_cpu_block(cfg, 8 + i, reps=0)
-    dt = (time.perf_counter() - t0) / args.steps * cfg["depth"]   # seconds per sample
+    step = DitCpuStep(cfg)
+    step.run(0)
+    times = [step.run(i + 1) for i in range(args.steps)]
+    dt = sum(times) / len(times)   # seconds per sample
     value = 1.0 / dt
-    sample = (f"each step: one DiT block of one sample fwd+bwd (float32 torch CPU restatement, "
-              f"{os.cpu_count()} threads) x {cfg['depth']} blocks")
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt, "higher_is_better": True,
+            "steps": args.steps, "warmup": 1, "ms_per_step": 1000 * dt, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": DIT_WORKLOAD, "global_batch": 1, "seq_len": DIT_T, "parallelism": "cpu"},
+            "config": dit_config_line(args, cfg),
             "cpu_baseline": {"value": value, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": sample},
+                             "sample": "each step: one " + dit_cpu_sample_note(os.cpu_count())},
             "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -728,10 +754,7 @@ def main_dit(args):
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": DIT_WORKLOAD + (f" (depth overridden to {cfg['depth']})" if args.depth else "")
-                       + (f" (adapters overridden to {args.adapter_type})" if args.adapter_type != "dora-rows" else ""),
-                       "global_batch": B * world, "seq_len": T,
-                       "parallelism": f"dp{world}", "l2": "256 MB flush between timed steps"},
+            "config": dit_config_line(args, cfg),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": None,
                          "kernel": "tcgen05 GEMM engine, classes linear.fwd + linear.dx (all frozen-base "
@@ -851,13 +874,211 @@ def main_attention(args):
     return 0
 
 
+# ------------------------------------------------------------------ single-kernel cases
+def gemm_case(a):
+    import numpy as np
+    import torch
+    import sa3k
+    import gguf_blocks
+    torch.cuda.set_device(0)
+    ctx = sa3k.Context(0)
+    ctx.set_option(sa3k.OPT_GEMM_PAIR, a.pair)
+    ctx.set_option(sa3k.OPT_GEMM_TILE_N, a.tile_n)
+    ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 1 if a.smem_dequant else 0)
+    g = torch.Generator().manual_seed(0)
+    W = torch.randn(a.n, a.k, generator=g) * 0.02                 # [out = n][in = k]
+    if a.qtype == "f32":
+        w = ctx.upload(W.numpy().view(np.uint8).reshape(a.n, -1), "f32", a.k, a.n)
+    else:
+        w = ctx.upload(gguf_blocks.encode(W.numpy(), a.qtype), a.qtype, a.k, a.n)
+    dev = torch.device("cuda", 0)
+    x = torch.randn(a.m, a.k, device=dev)
+    y = torch.empty(a.m, a.n, device=dev)
+    ad = None
+    if a.adapter:
+        A = torch.randn(16, a.k, device=dev) * 0.02
+        Bm = torch.randn(a.n, 16, device=dev) * 0.02
+        ad = ctx.adapter(A, Bm, 1.0)
+    if a.dx:
+        dy = torch.randn(a.m, a.n, device=dev)
+        dx = torch.empty(a.m, a.k, device=dev)
+        gA = torch.zeros(16, a.k, device=dev) if ad else None
+        gB = torch.zeros(a.n, 16, device=dev) if ad else None
+        run = lambda: ctx.linear_bwd(w, x, y, dy, dx, ad=ad, dA=gA, dB=gB)
+        flops = 2.0 * a.m * a.n * a.k
+    else:
+        run = lambda: ctx.linear_fwd(w, x, y, ad=ad)
+        flops = 2.0 * a.m * a.n * a.k
+    for _ in range(a.warmup):
+        run()
+    ctx.sync()
+    if a.time:
+        ctx.profile_enable(timing=1)
+    for _ in range(a.reps):
+        run()
+    ctx.sync()
+    if a.time:
+        pr = ctx.profile_read()
+        name = "linear.dx" if a.dx else "linear.fwd"
+        n, ms = pr[name]
+        print(f"{'dx' if a.dx else 'fwd'} {a.m}x{a.n}x{a.k} {a.qtype} pair{a.pair} bn{a.tile_n}: "
+              f"{ms / n * 1e3:.1f} us/launch, {flops * n / (ms / 1e3) / 1e12:.1f} TFLOP/s")
+        for other, (n2, ms2) in sorted(pr.items()):
+            if other != name:
+                print(f"    {other}: {n2 // a.reps} launch(es) per call, {ms2 / a.reps * 1e3:.1f} us per call")
+    w.free()
+    ctx.close()
+
+
+def attn_dit_case(a):
+    """Self-attention of the DiT step: B x H heads of Sq = Sk tokens, head_dim 64, q / k / v /
+    o as [B][S][H * 64] f16 (the layout of the fused projection), forward and backward."""
+    import torch
+    import sa3k
+    torch.cuda.set_device(0)
+    ctx = sa3k.Context(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    B, H, S = a.b, a.h, a.s
+    bf = lambda: torch.randn(B, S, H * 64, generator=g, device="cuda").to(torch.float16)
+    q, k, v, dO = bf(), bf(), bf(), bf()
+    o = torch.empty_like(q)
+    dq, dk, dv = (torch.empty(B, S, H * 64, device="cuda") for _ in range(3))
+    lse = torch.empty(B * H * S, device="cuda")
+    st = (S * H * 64, 64, H * 64)
+    T4 = sa3k.t4
+    fwd = lambda: ctx.attention_fwd(B, H, S, S, 0.125, a.window, T4(q, *st), T4(k, *st), T4(v, *st), T4(o, *st), lse)
+    bwd = lambda: ctx.attention_bwd(B, H, S, S, 0.125, a.window, T4(q, *st), T4(k, *st), T4(v, *st), T4(o, *st),
+                                    T4(dO, *st), lse, T4(dq, *st), T4(dk, *st), T4(dv, *st))
+    for _ in range(a.warmup):
+        fwd()
+        bwd()
+    ctx.sync()
+    if a.time:
+        ctx.profile_enable(timing=1)
+    for _ in range(a.reps):
+        fwd()
+        if not a.fwd_only:
+            bwd()
+    ctx.sync()
+    if a.time:
+        for name, (n, ms) in sorted(ctx.profile_read().items()):
+            print(f"attention B{B} H{H} S{S} window {a.window}: {name} {ms / n * 1e3:.1f} us/launch")
+    ctx.close()
+
+
+def mat_case(a):
+    import torch
+    import sa3k
+    import gguf_blocks
+    torch.cuda.set_device(0)
+    ctx = sa3k.Context(0)
+    g = torch.Generator().manual_seed(0)
+    n, k, m, r = a.n, a.k, a.m, a.rank
+    W = torch.randn(n, k, generator=g) * 0.02
+    w = ctx.upload(gguf_blocks.encode(W.numpy(), a.qtype), a.qtype, k, n)
+    dev = torch.device("cuda", 0)
+    t = lambda *shape: torch.randn(*shape, device=dev) * 0.02
+    xs = a.type.endswith("-xs")
+    fam = a.type[:-3] if xs else a.type
+    p = dict(U=t(n, r), V=t(k, r), M=t(r, r)) if xs else dict(A=t(r, k), B=t(n, r))
+    grads = dict(dM=torch.empty(r, r, device=dev)) if xs else dict(dA=torch.empty(r, k, device=dev),
+                                                                     dB=torch.empty(n, r, device=dev))
+    if fam == "dora-rows":
+        p["m"], grads["dm"] = torch.ones(n, device=dev), torch.empty(n, device=dev)
+    elif fam == "dora-cols":
+        p["m"], grads["dm"] = torch.ones(k, device=dev), torch.empty(k, device=dev)
+    elif fam == "bora":
+        p["m_r"], p["m_c"] = torch.ones(n, device=dev), torch.ones(k, device=dev)
+        grads["dm_r"], grads["dm_c"] = torch.empty(n, device=dev), torch.empty(k, device=dev)
+    ad = ctx.mat_adapter(a.type, r, 1.0, **p)
+    x, dy = torch.randn(m, k, device=dev), torch.randn(m, n, device=dev)
+    y, dx = torch.empty(m, n, device=dev), torch.empty(m, k, device=dev)
+    run = lambda: ctx.linear_mat_fwd_bwd(w, ad, x, dy, y=y, dx=dx, **grads)
+    for _ in range(a.warmup):
+        run()
+    ctx.sync()
+    if a.time:
+        ctx.profile_enable(timing=1)
+    for _ in range(a.reps):
+        run()
+    ctx.sync()
+    if a.time:
+        E = n * k
+        code = {"q8_0": 1.0 + 4.0 / 32, "q4_k": 0.5 + 8.0 / 32}[a.qtype]
+        work = {"mat.build": (E * (code + 4), "B"), "mat.cols": (E * 4, "B"), "mat.weff": (E * 6, "B"),
+                "mat.transpose": (m * n * 4, "B"), "mat.cols_bwd": (E * 8, "B"), "mat.rows_bwd": (E * 10, "B"),
+                "mat.dA": (2.0 * E * r, "F"), "mat.dB": (2.0 * E * r, "F"), "mat.fwd": (2.0 * m * n * k, "F"),
+                "mat.dx": (2.0 * m * n * k, "F"), "mat.dW": (2.0 * m * n * k, "F")}
+        total = 0.0
+        print(f"mat {a.type} {a.qtype} tokens {m}, in {k}, out {n}, rank {r}")
+        for name, (cnt, ms) in sorted(ctx.profile_read().items()):
+            us = ms / a.reps * 1e3
+            total += us
+            amt, kind = work.get(name, (0, ""))
+            rate = (f"{amt * cnt / a.reps / (us * 1e-6) / 1e9:8.0f} GB/s (algorithmic)" if kind == "B" else
+                    f"{amt * cnt / a.reps / (us * 1e-6) / 1e12:8.0f} TFLOP/s" if kind == "F" else "")
+            print(f"    {name:14s} {cnt // a.reps} launch(es) {us:8.1f} us  {rate}")
+        print(f"    total {total:.1f} us per call")
+    w.free()
+    ctx.close()
+
+
+def kernel_case(workload, argv):
+    """Single-kernel cases for profiling and tuning (a profiler such as ncu -k regex:gemm_tc -c 1 sees
+    a handful of launches of one kernel on a few hundred MB), run through the C ABI:
+
+      --workload gemm [--m 4352 --n 1536 --k 1536] [--dx] [--qtype f32|q8_0|q4_k] [--pair 0|1|2]
+                      [--tile-n 0|128|192|256] [--adapter] [--smem-dequant] [--reps 3] [--time]
+          one frozen-base linear: the forward y = x W^T, or with --dx the input gradient
+          dx[m][k] = dy[m][n] W[n][k] (in = k, out = n); --adapter adds a rank-16 LoRA adapter;
+          --smem-dequant reads a quantized base as its codes, dequantized in shared memory
+      --workload attn-dit [--b 4 --h 24 --s 1088 --window -1] [--fwd-only]
+          the DiT step's self-attention, q / k / v / o as [B][S][H * 64] f16, forward + backward
+      --workload mat --type bora [--m 1024 --n 1536 --k 1536 --rank 16] [--qtype q8_0|q4_k]
+          forward + backward of a linear with a materialized adapter (W_eff rebuilt every call)
+
+    --time prints the CUDA-event time per launch class (not to be used under a profiler)."""
+    ap = argparse.ArgumentParser(prog=f"bench.py --workload {workload}")
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--time", action="store_true")
+    if workload == "gemm":
+        ap.add_argument("--m", type=int, default=4352)
+        ap.add_argument("--n", type=int, default=1536)
+        ap.add_argument("--k", type=int, default=1536)
+        ap.add_argument("--dx", action="store_true")
+        ap.add_argument("--qtype", default="f32", choices=["f32", "q8_0", "q4_k"])
+        ap.add_argument("--pair", type=int, default=1)
+        ap.add_argument("--tile-n", type=int, default=0)
+        ap.add_argument("--adapter", action="store_true")
+        ap.add_argument("--smem-dequant", action="store_true")
+        return gemm_case(ap.parse_args(argv))
+    if workload == "attn-dit":
+        ap.add_argument("--b", type=int, default=4)
+        ap.add_argument("--h", type=int, default=24)
+        ap.add_argument("--s", type=int, default=1088)
+        ap.add_argument("--window", type=int, default=-1)
+        ap.add_argument("--fwd-only", action="store_true")
+        return attn_dit_case(ap.parse_args(argv))
+    ap.add_argument("--type", default="bora")
+    ap.add_argument("--m", type=int, default=1024)
+    ap.add_argument("--n", type=int, default=1536)
+    ap.add_argument("--k", type=int, default=1536)
+    ap.add_argument("--rank", type=int, default=16)
+    ap.add_argument("--qtype", default="q8_0", choices=["q8_0", "q4_k"])
+    return mat_case(ap.parse_args(argv))
+
+
+KERNEL_CASES = ("gemm", "attn-dit", "mat")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="sa3k", choices=["sa3k", "reference"])
-    ap.add_argument("--workload", default="dit", choices=["dit", "linear", "attention"])
+    ap.add_argument("--workload", default="dit", choices=["dit", "linear", "attention", *KERNEL_CASES])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--depth", type=int, default=0,
                     help="dit: override the block count (small device footprint for ncu captures of per-block "
@@ -867,7 +1088,11 @@ def main():
                          "materialized families time their per-step W_eff build and weight-gradient passes)")
     ap.add_argument("--profile-step", action="store_true",
                     help="dit: bracket one extra graph replay with cudaProfilerStart/Stop (for ncu --profile-from-start off)")
-    args = ap.parse_args()
+    args, rest = ap.parse_known_args()
+    if args.workload in KERNEL_CASES:   # profiling harness, not a benchmark line
+        return kernel_case(args.workload, [a for a in sys.argv[1:] if a not in ("--workload", args.workload)])
+    if rest:
+        ap.error(f"unrecognized arguments: {' '.join(rest)}")
     args.warmup = max(args.warmup, 3)
     if args.workload == "linear":
         return run_linear_reference(args) if args.impl == "reference" else main_linear(args)
