@@ -90,6 +90,15 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       while the stream is being captured, or with profiling timing on, run eagerly.
  *       0: every call launches its kernels one by one. */
 #define SA3K_OPT_STEP_GRAPH 7
+/* SA3K_OPT_DEQUANT_TMEM  1 (default): GEMMs that dequantize a Q8_0 / Q4_K base in the kernel (see
+ *       SA3K_OPT_SMEM_DEQUANT; also every GEMM over a quantized base uploaded without the f16
+ *       cache) compute the transposed product with the weight as the tensor-memory operand: the
+ *       codes are read from global memory, dequantized in registers and written to tensor memory,
+ *       so only the activation tile passes through shared memory.  The input-gradient GEMM reads a
+ *       transposed copy of the codes, made once on its first eager call (1 byte per weight for
+ *       Q8_0, half for Q4_K).  0: dequantize into a shared-memory B tile instead.  Results are
+ *       identical up to the order of the f32 accumulation. */
+#define SA3K_OPT_DEQUANT_TMEM 8
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded
@@ -497,9 +506,13 @@ typedef struct sa3k_dp_comm sa3k_dp_comm;
 
 /* 128 opaque bytes made on one rank and handed to every rank (by the caller's own means). */
 int sa3k_dp_unique_id(void* out, int out_len, char* err, int err_len);
-/* Collective over all nranks processes (each with its own context / device). */
+/* Collective over all nranks processes (each with its own context / device).  The rendezvous is
+ * bounded: a communicator whose ranks have not all joined within 300 s is aborted and the call
+ * returns an error (sa3k_dp_comm_create_timeout sets the bound). */
 int sa3k_dp_comm_create(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id,
                         sa3k_dp_comm** out, char* err, int err_len);
+int sa3k_dp_comm_create_timeout(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id,
+                                double timeout_s, sa3k_dp_comm** out, char* err, int err_len);
 void sa3k_dp_comm_destroy(sa3k_dp_comm* comm);
 int sa3k_dp_comm_info(const sa3k_dp_comm* comm, int* nranks, int* rank);
 /* In-place sum of buf[n] (f32, device) over all ranks, on the context's stream. */

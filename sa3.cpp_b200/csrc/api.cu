@@ -260,6 +260,7 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
     case SA3K_OPT_ATTN_TC: ctx->c.attn_tc = value != 0; return 0;
     case SA3K_OPT_PDL: ctx->c.pdl = value != 0; return 0;
     case SA3K_OPT_STEP_GRAPH: ctx->c.step_graph = value != 0; return 0;
+    case SA3K_OPT_DEQUANT_TMEM: ctx->c.dequant_tmem = value != 0; return 0;
     default: return fill_err(err, err_len, "unknown option");
   }
 }
@@ -342,6 +343,7 @@ int sa3k_weight_upload(sa3k_ctx* ctx, int type, const void* blocks, int64_t in, 
     if (w.codes) cudaFree(w.codes);
     if (w.scales) cudaFree(w.scales);
     if (w.f16) cudaFree(w.f16);
+    if (w.codes_t) cudaFree(w.codes_t);
     delete h;
     cudaGetLastError();
     return fill_err(err, err_len, msg);
@@ -382,6 +384,7 @@ void sa3k_weight_free(sa3k_weight* h) {
   if (w.codes) cudaFree(w.codes);
   if (w.scales) cudaFree(w.scales);
   if (w.f16) cudaFree(w.f16);
+  if (w.codes_t) cudaFree(w.codes_t);
   delete h;
 }
 

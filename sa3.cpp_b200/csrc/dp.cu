@@ -16,6 +16,9 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <time.h>
+#include <unistd.h>
+
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -27,7 +30,9 @@ struct NcclApi {
   bool loaded = false;
   std::string error;
   ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
-  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_init_rank_config)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*) = nullptr;
+  ncclResult_t (*get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
   ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                              cudaStream_t) = nullptr;
@@ -52,7 +57,9 @@ const NcclApi* nccl(std::string& err) {
       g_nccl.error = std::string("cannot load NCCL (libnccl.so.2 or SA3K_NCCL_LIBRARY): ") + (e ? e : "");
       return;
     }
-    if (!bind(h, "ncclGetUniqueId", g_nccl.get_unique_id) || !bind(h, "ncclCommInitRank", g_nccl.comm_init_rank) ||
+    if (!bind(h, "ncclGetUniqueId", g_nccl.get_unique_id) ||
+        !bind(h, "ncclCommInitRankConfig", g_nccl.comm_init_rank_config) ||
+        !bind(h, "ncclCommGetAsyncError", g_nccl.get_async_error) || !bind(h, "ncclCommAbort", g_nccl.comm_abort) ||
         !bind(h, "ncclCommDestroy", g_nccl.comm_destroy) || !bind(h, "ncclAllReduce", g_nccl.all_reduce) ||
         !bind(h, "ncclGetErrorString", g_nccl.error_string)) {
       g_nccl.error = "the loaded NCCL library lacks a required symbol";
@@ -79,6 +86,27 @@ std::string nccl_msg(const NcclApi* api, const char* what, ncclResult_t r) {
   return std::string(what) + ": " + (api->error_string ? api->error_string(r) : "NCCL error");
 }
 
+double now_s() {
+  timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return (double)t.tv_sec + 1e-9 * (double)t.tv_nsec;
+}
+
+// A non-blocking communicator's pending operation: poll its state until it leaves ncclInProgress
+// or the deadline passes (then the caller aborts the communicator).
+ncclResult_t settle(const NcclApi* api, ncclComm_t comm, double deadline) {
+  ncclResult_t st = ncclInProgress;
+  while (true) {
+    if (api->get_async_error(comm, &st) != ncclSuccess) return ncclSystemError;
+    if (st != ncclInProgress) return st;
+    if (now_s() > deadline) return ncclInProgress;
+    usleep(1000);
+  }
+}
+
+constexpr double kInitTimeoutS = 300.0;   // sa3k_dp_comm_create's bound on the rendezvous
+constexpr double kOpTimeoutS = 60.0;      // bound on enqueueing one collective
+
 }  // namespace
 
 struct sa3k_dp_comm {
@@ -101,10 +129,11 @@ int sa3k_dp_unique_id(void* out, int out_len, char* err, int err_len) {
   return 0;
 }
 
-int sa3k_dp_comm_create(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id, sa3k_dp_comm** out,
-                        char* err, int err_len) {
+int sa3k_dp_comm_create_timeout(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id, double timeout_s,
+                                sa3k_dp_comm** out, char* err, int err_len) {
   if (!ctx || !unique_id || !out) return fail(err, err_len, "NULL argument");
   if (nranks < 1 || rank < 0 || rank >= nranks) return fail(err, err_len, "rank must be in [0, nranks)");
+  if (!(timeout_s > 0.0)) return fail(err, err_len, "timeout must be positive");
   std::string e;
   const NcclApi* api = nccl(e);
   if (!api) return fail(err, err_len, e);
@@ -115,13 +144,30 @@ int sa3k_dp_comm_create(sa3k_ctx* ctx, int nranks, int rank, const void* unique_
   c->nranks = nranks;
   c->rank = rank;
   c->device = ctx->c.device;
-  const ncclResult_t r = api->comm_init_rank(&c->comm, nranks, id, rank);
+  // a non-blocking communicator: the rendezvous runs in the background and is polled against the
+  // deadline, so a peer that never joins ends in an error here instead of a hang
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclResult_t r = api->comm_init_rank_config(&c->comm, nranks, id, rank, &cfg);
+  if (r == ncclInProgress || r == ncclSuccess) r = c->comm ? settle(api, c->comm, now_s() + timeout_s) : r;
   if (r != ncclSuccess) {
+    if (c->comm) api->comm_abort(c->comm);
     delete c;
-    return fail(err, err_len, nccl_msg(api, "ncclCommInitRank", r));
+    if (r == ncclInProgress) {
+      char msg[160];
+      std::snprintf(msg, sizeof msg, "ncclCommInitRankConfig: the %d ranks did not all join within %.1f s (aborted)",
+                    nranks, timeout_s);
+      return fail(err, err_len, msg);
+    }
+    return fail(err, err_len, nccl_msg(api, "ncclCommInitRankConfig", r));
   }
   *out = c;
   return 0;
+}
+
+int sa3k_dp_comm_create(sa3k_ctx* ctx, int nranks, int rank, const void* unique_id, sa3k_dp_comm** out,
+                        char* err, int err_len) {
+  return sa3k_dp_comm_create_timeout(ctx, nranks, rank, unique_id, kInitTimeoutS, out, err, err_len);
 }
 
 void sa3k_dp_comm_destroy(sa3k_dp_comm* comm) {
@@ -144,7 +190,9 @@ int sa3k_dp_allreduce_sum(sa3k_ctx* ctx, sa3k_dp_comm* comm, float* buf, int64_t
   const NcclApi* api = nccl(e);
   if (!api) return fail(err, err_len, e);
   cudaSetDevice(ctx->c.device);
-  const ncclResult_t r = api->all_reduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, comm->comm, ctx->c.stream);
+  ncclResult_t r = api->all_reduce(buf, buf, (size_t)n, ncclFloat32, ncclSum, comm->comm, ctx->c.stream);
+  if (r == ncclInProgress) r = settle(api, comm->comm, now_s() + kOpTimeoutS);   // non-blocking enqueue
+  if (r == ncclInProgress) return fail(err, err_len, "ncclAllReduce: not enqueued within the time limit");
   if (r != ncclSuccess) return fail(err, err_len, nccl_msg(api, "ncclAllReduce", r));
   return 0;
 }

@@ -1,8 +1,10 @@
 // gemm_tc.cu -- host side of the tcgen05 GEMM engine: tensor maps, tile choice, launch.
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_wq.cuh"
 #include "sa3k_internal.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <mutex>
@@ -267,6 +269,68 @@ static int pick_bn(const Ctx* c, int M, int N, bool quant) {
   return best;
 }
 
+// A GEMM over a quantized base with the weight dequantized into tensor memory (gemm_wq.cuh): the
+// forward y = x W^T (NT) or the input gradient dx = dy W (TN, from the transposed codes).
+static int gemm_wq(Ctx* c, const GemmDesc& d, std::string& err) {
+  Weight* w = const_cast<Weight*>(d.w);   // the transposed codes are a lazily made cache
+  const bool nt = d.bsrc == kB_WEIGHT_NT;
+  const bool q4 = w->type == kTypeQ4_K;
+  if (d.a_mn) { err = "gemm: MN-major A is not supported with an in-kernel dequantized base"; return 1; }
+  if (!nt && weight_transpose_codes(c, w, err)) return 1;
+  const auto F16 = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const auto SW = CU_TENSOR_MAP_SWIZZLE_128B;
+  const auto NOSW = CU_TENSOR_MAP_SWIZZLE_NONE;
+  const auto SCT = q4 ? CU_TENSOR_MAP_DATA_TYPE_UINT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  const long sc_elem = q4 ? 8 : 4;
+  // codes as [N features][code_ld bytes]: 64 (Q8_0) or 32 (Q4_K) bytes of k per feature per stage
+  const void* codes = nt ? (const void*)w->codes : (const void*)w->codes_t;
+  const long code_ld = nt ? (q4 ? w->in / 2 : w->in) : (q4 ? w->out / 2 : w->out);
+  CUtensorMap tx, tc, tsc, tu;
+  if (make_map(&tx, F16, d.a, d.K, d.M, d.lda * 2, 64, kWqT, SW, "activation", err)) return 1;
+  if (make_map(&tc, U8, codes, code_ld, d.N, code_ld, q4 ? kWqK / 2 : kWqK, kWqF,
+               q4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, "codes", err))
+    return 1;
+  // scales [in/32][out]: NT boxes of 4 k-blocks x 128 features, TN of 4 feature blocks x 128 k
+  if (nt) {
+    if (make_map(&tsc, SCT, w->scales, w->out, w->in / 32, w->out * sc_elem, kWqF, 4, NOSW, "scales", err)) return 1;
+  } else {
+    if (make_map(&tsc, SCT, w->scales, w->out, w->in / 32, w->out * sc_elem, kWqK, 4, NOSW, "scales", err)) return 1;
+  }
+  if (d.ext_at) {
+    if (make_map(&tu, F16, d.ext_at, d.M, 16, d.ld_ext * 2, 64, 16, SW, "ext u^T", err)) return 1;
+  } else {
+    tu = tx;
+  }
+  WqArgs a;
+  a.M = d.M; a.N = d.N; a.K = d.K;
+  a.nt = nt ? 1 : 0;
+  a.has_ext = d.ext_at ? 1 : 0;
+  a.ext_b = d.ext_b;
+  a.col_scale = d.col_scale; a.col_bias = d.col_bias; a.alpha = d.alpha;
+  a.out = d.out; a.ldo = d.ldo; a.out_trans = d.out_trans; a.accumulate = d.accumulate;
+  a.out_h = d.out_h; a.ldo_h = d.ldo_h; a.out_h_trans = d.out_h_trans; a.h_scale = d.h_scale;
+  a.out_h_t = d.out_h_t; a.ldo_h_t = d.ldo_h_t;
+  a.err = c->d_err;
+  const long tiles = (long)((d.N + kWqF - 1) / kWqF) * ((d.M + kWqT - 1) / kWqT);
+  const unsigned grid = (unsigned)std::min<long>(tiles, (long)c->sm_count);
+  auto launch_q = [&](auto kern, int dyn) -> int {
+    if (smem_attr(reinterpret_cast<const void*>(kern), dyn, c->device, "gemm_wq smem attribute", err)) return 1;
+    ProfScope prof_(c, d.name);
+    launch_pdl(c, kern, dim3(grid), dim3(kWqThreads), (size_t)dyn, tx, tc, tsc, tu, a);
+    return check_launch("gemm_wq", err);
+  };
+  return q4 ? launch_q(gemm_wq_kernel<1>, WqSmem<1>::DYN) : launch_q(gemm_wq_kernel<0>, WqSmem<0>::DYN);
+}
+
+// The tensor-memory dequant kernel reads the codes by TMA: their rows must be 16-byte multiples.
+static bool wq_fits(const GemmDesc& d) {
+  const Weight* w = d.w;
+  const bool q4 = w->type == kTypeQ4_K;
+  const long code_ld = d.bsrc == kB_WEIGHT_NT ? (q4 ? w->in / 2 : w->in) : (q4 ? w->out / 2 : w->out);
+  return !d.a_mn && code_ld % 16 == 0 && (!q4 || d.bsrc == kB_WEIGHT_NT || w->out % 2 == 0);
+}
+
 int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   if (d.M <= 0 || d.N <= 0 || d.K < 0 || (d.K == 0 && !d.ext_at)) {
     err = "gemm: need M, N > 0 and K > 0";
@@ -277,6 +341,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   // and the context has not asked for the in-smem path explicitly
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
                      !(d.w->f16 && !c->smem_dequant);
+  if (quant && c->dequant_tmem && wq_fits(d)) return gemm_wq(c, d, err);
   int bn = d.bn;
   if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N, quant);
   if (quant && bn == 192) bn = 256;

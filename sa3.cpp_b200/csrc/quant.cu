@@ -143,6 +143,73 @@ int weight_repack(Ctx* c, Weight* w, std::string& err) {
   return check_launch("weight repack", err);
 }
 
+// codes_t[i][o] = codes[o][i] (Q8_0 bytes, or Q4_K nibbles: codes_t byte i*(out/2) + o/2 holds o
+// even in the low nibble), one 64 x 64 tile of elements per block through shared memory.
+__global__ void transpose_codes_kernel(const uint8_t* __restrict__ codes, int64_t in, int64_t out, int q4,
+                                       uint8_t* __restrict__ codes_t) {
+  __shared__ uint8_t tile[64][65];
+  const int64_t o0 = (int64_t)blockIdx.y * 64, i0 = (int64_t)blockIdx.x * 64;
+  for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+    const int r = e / 64, cl = e % 64;   // element (o0 + r, i0 + cl)
+    const int64_t o = o0 + r, i = i0 + cl;
+    uint8_t v = 0;
+    if (o < out && i < in) {
+      if (q4) {
+        const uint8_t b = codes[o * (in / 2) + i / 2];
+        v = (i & 1) ? (uint8_t)(b >> 4) : (uint8_t)(b & 0x0F);
+      } else {
+        v = codes[o * in + i];
+      }
+    }
+    tile[r][cl] = v;
+  }
+  __syncthreads();
+  if (q4) {
+    for (int e = threadIdx.x; e < 64 * 32; e += blockDim.x) {
+      const int cl = e / 32, rp = e % 32;   // output row i0 + cl, byte (o0 + 2 rp) / 2
+      const int64_t i = i0 + cl, o = o0 + 2 * rp;
+      if (i < in && o < out) codes_t[i * (out / 2) + o / 2] = (uint8_t)(tile[2 * rp][cl] | (tile[2 * rp + 1][cl] << 4));
+    }
+  } else {
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+      const int cl = e / 64, r = e % 64;
+      const int64_t i = i0 + cl, o = o0 + r;
+      if (i < in && o < out) codes_t[i * out + o] = tile[r][cl];
+    }
+  }
+}
+
+int weight_transpose_codes(Ctx* c, Weight* w, std::string& err) {
+  if (w->codes_t) return 0;
+  if (w->type != kTypeQ8_0 && w->type != kTypeQ4_K) {
+    err = "transposed codes exist only for Q8_0 / Q4_K weights";
+    return 1;
+  }
+  const bool q4 = w->type == kTypeQ4_K;
+  if (q4 && (w->out & 1)) {
+    err = "Q4_K transposed codes need an even out";
+    return 1;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    err = "transposed weight codes are made on the first eager call, not inside a stream capture";
+    return 1;
+  }
+  const size_t bytes = q4 ? (size_t)(w->in * (w->out / 2)) : (size_t)(w->in * w->out);
+  if (cudaMalloc(&w->codes_t, bytes) != cudaSuccess) {
+    w->codes_t = nullptr;
+    cudaGetLastError();
+    err = "out of device memory (transposed weight codes)";
+    return 1;
+  }
+  ProfScope prof_(c, "weight transpose");
+  dim3 grid((unsigned)((w->in + 63) / 64), (unsigned)((w->out + 63) / 64));
+  transpose_codes_kernel<<<grid, 256, 0, c->stream>>>(reinterpret_cast<const uint8_t*>(w->codes), w->in, w->out,
+                                                       q4 ? 1 : 0, reinterpret_cast<uint8_t*>(w->codes_t));
+  return check_launch("weight transpose", err);
+}
+
 int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err) {
   ProfScope prof_(c, "dequant");
   dequant_kernel<<<1184, 256, 0, c->stream>>>(*w, dst);

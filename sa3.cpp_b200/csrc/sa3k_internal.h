@@ -26,6 +26,9 @@ struct Weight {
   float* scales = nullptr;           // Q8_0 f32 [in/32][out] | Q4_K float2 [in/32][out]
   __half* f16 = nullptr;     // f16 [out][in] operand copy (F16/F32 always; Q8_0/Q4_K
                                      // when the context keeps a dequantized cache)
+  int8_t* codes_t = nullptr;         // Q8_0 int8 [in][out] | Q4_K nibble pairs [in][out/2]: the codes
+                                     // transposed, made on the first input-gradient GEMM that
+                                     // dequantizes in the kernel (gemm_wq)
   int device = 0;
 };
 
@@ -61,6 +64,7 @@ struct Ctx {
   bool attn_tc = true;               // tcgen05 attention kernels (else the mma.sync ones)
   bool pdl = true;                   // programmatic dependent launch between consecutive kernels
   bool step_graph = true;            // the DiT step records and replays a CUDA graph
+  bool dequant_tmem = true;          // in-kernel dequantization into tensor memory (gemm_wq)
   // bumped whenever something a recorded graph may depend on changes: an option, a scratch
   // buffer reallocated, the RoPE table rebuilt
   uint64_t gen = 0;
@@ -137,6 +141,8 @@ enum : int { kSlotSplitK = 63, kSlotHeadSlices = 62, kSlotRope = 61, kSlotSplitC
 void* scratch_get(Ctx* c, int slot, size_t bytes, std::string& err);
 
 int weight_repack(Ctx* c, Weight* w, std::string& err);
+// codes_t of a Q8_0 / Q4_K weight (allocated and filled once; a no-op when present)
+int weight_transpose_codes(Ctx* c, Weight* w, std::string& err);
 int weight_cache_f16(Ctx* c, Weight* w, std::string& err);
 int weight_dequant(Ctx* c, const Weight* w, float* dst, std::string& err);
 int weight_row_norms(Ctx* c, const Weight* w, float eps, float* nsq, float* nrm, std::string& err);

@@ -24,7 +24,7 @@ ABI_SYMBOLS = (
     "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_attention_bwd_noalloc", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
     "sa3k_dit_create", "sa3k_dit_free", "sa3k_dit_set_tensor", "sa3k_dit_init_adapters", "sa3k_dit_adapter_size",
     "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
-    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create",
+    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create", "sa3k_dp_comm_create_timeout",
     "sa3k_dp_comm_destroy", "sa3k_dp_comm_info", "sa3k_dp_allreduce_sum", "sa3k_dp_allreduce_adamw",
     "sa3k_dit_dp_apply_adamw", "sa3k_dit_save_adapter", "sa3k_dit_load_adapter", "sa3k_dit_save_checkpoint",
     "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
@@ -34,6 +34,7 @@ ABI_SYMBOLS = (
 )
 OPT_WEIGHT_F16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
+OPT_DEQUANT_TMEM = 8
 
 
 class Sa3kError(RuntimeError):
@@ -162,6 +163,7 @@ def lib():
         L.sa3k_head_prep_bwd.argtypes = [P, P, I64, P, I, I, I, ctypes.POINTER(HeadSliceC), I, I, F, P, E, I]
         L.sa3k_dp_unique_id.argtypes = [P, I, E, I]
         L.sa3k_dp_comm_create.argtypes = [P, I, I, P, ctypes.POINTER(P), E, I]
+        L.sa3k_dp_comm_create_timeout.argtypes = [P, I, I, P, ctypes.c_double, ctypes.POINTER(P), E, I]
         L.sa3k_dp_comm_destroy.argtypes = [P]
         L.sa3k_dp_comm_destroy.restype = None
         L.sa3k_dp_comm_info.argtypes = [P, ctypes.POINTER(I), ctypes.POINTER(I)]
@@ -584,13 +586,18 @@ def dp_unique_id():
 class DpComm:
     """A data-parallel communicator of nranks processes, one per GPU (sa3k_dp_comm_*)."""
 
-    def __init__(self, ctx, nranks, rank, unique_id):
+    def __init__(self, ctx, nranks, rank, unique_id, timeout_s=None):
+        """timeout_s: bound on the rendezvous (every rank must join within it; default 300 s)."""
         assert len(unique_id) == 128
         self.ctx = ctx
         self._h = ctypes.c_void_p()
         uid = ctypes.create_string_buffer(bytes(unique_id), 128)
         err = ctypes.create_string_buffer(512)
-        _check(lib().sa3k_dp_comm_create(ctx._h, nranks, rank, uid, ctypes.byref(self._h), err, 512), err)
+        if timeout_s is None:
+            _check(lib().sa3k_dp_comm_create(ctx._h, nranks, rank, uid, ctypes.byref(self._h), err, 512), err)
+        else:
+            _check(lib().sa3k_dp_comm_create_timeout(ctx._h, nranks, rank, uid, float(timeout_s),
+                                                     ctypes.byref(self._h), err, 512), err)
         self.nranks, self.rank = nranks, rank
         ctx._own(self)
 

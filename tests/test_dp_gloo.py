@@ -127,3 +127,33 @@ def test_empty_batch_is_an_error():
     tr.begin()
     with pytest.raises(ValueError):
         tr.apply(HP)
+
+
+def _absent_peer_worker(rank, world, port, outdir):
+    """Rank 1 joins the process group and leaves without taking part in the clique-id exchange;
+    rank 0 must get an error from the exchange within the group's timeout instead of waiting."""
+    import time
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=3))
+    if rank == 1:
+        return   # leaves between steps: no collective of its own is in flight
+    import dp
+    import sa3k
+    t0 = time.monotonic()
+    try:
+        dp.exchange_unique_id(rank, sa3k.dp_unique_id, dist.broadcast_object_list)
+        outcome = "returned"
+    except Exception as e:   # gloo reports the timeout or the closed peer connection
+        outcome = f"raised {type(e).__name__}"
+    with open(os.path.join(outdir, "r0.txt"), "w") as f:
+        f.write(f"{outcome}\n{time.monotonic() - t0:.3f}\n")
+
+
+def test_absent_peer_ends_the_exchange_with_an_error(sa3k_lib):
+    import torch.multiprocessing as mp
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_absent_peer_worker, args=(2, _free_port(), d), nprocs=2, start_method="spawn")
+        lines = open(os.path.join(d, "r0.txt")).read().splitlines()
+        assert lines[0].startswith("raised"), lines
+        assert float(lines[1]) < 60.0

@@ -222,3 +222,27 @@ def test_step_graph_replay_matches_eager(ctx):
         np.testing.assert_allclose(loss, res[0][0], rtol=1e-5)
         assert rel_l2(g, res[0][1]) < 1e-5
     dit.close()
+
+
+@pytest.mark.parametrize("differential", [0, 1])
+def test_step_in_kernel_dequant_matches_cache(ctx, differential):
+    """The step with every frozen-base GEMM dequantizing the Q8_0 codes in the kernel (the weight
+    as the tensor-memory operand, SA3K_OPT_SMEM_DEQUANT) computes the same products as the step on
+    the f16 operand cache: losses and gradients agree to the f32 accumulation order."""
+    import sa3k
+    res = []
+    for smem in (0, 1):
+        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, smem)
+        dit, deq, ad, targets, rng = _build(ctx, dict(CFG, differential=differential), scope="full")
+        inputs = _inputs(rng)
+        dit.zero_grads()
+        loss = np.zeros(B, np.float32)
+        dit.forward_backward(B, T, CTX, *inputs, loss=loss)
+        ctx.sync()
+        g = np.zeros(dit.size(), np.float32)
+        dit.copy(1, g, to_model=False)
+        res.append((loss, g))
+        dit.close()
+    ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
+    np.testing.assert_allclose(res[1][0], res[0][0], rtol=1e-5)
+    assert rel_l2(res[1][1], res[0][1]) < 1e-4

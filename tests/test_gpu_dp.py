@@ -103,3 +103,25 @@ def test_two_gpu_dp_step_matches_one_gpu(ctx):
     rel = np.linalg.norm(upd_dp - upd_one) / np.linalg.norm(upd_one)
     assert rel < 1e-2, rel
     assert np.abs(upd_dp - upd_one).max() <= 2 * STEPS * 1e-3 + 1e-6
+
+
+@pytest.mark.timeout(180, method="thread")
+def test_comm_rendezvous_without_peer_times_out(ctx):
+    """A two-rank communicator whose second rank never joins: the bounded rendezvous aborts the
+    NCCL communicator and reports an error within its limit, and the context stays usable (one
+    GPU; nothing runs on the device while the rendezvous waits)."""
+    import time
+    import torch
+    import sa3k
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    uid = sa3k.dp_unique_id()
+    t0 = time.monotonic()
+    with pytest.raises(sa3k.Sa3kError, match="did not all join"):
+        sa3k.DpComm(ctx, 2, 0, uid, timeout_s=3.0)
+    assert time.monotonic() - t0 < 60.0
+    p = torch.zeros(64, device="cuda")
+    g = torch.ones(64, device="cuda")
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    ctx.adamw(p, g, m, v, sa3k.AdamWParams(1e-3, 0.9, 0.999, 1e-8, 0.0, 0.0), 1)
+    ctx.sync()
+    assert torch.allclose(p, torch.full_like(p, -1e-3), rtol=1e-4)

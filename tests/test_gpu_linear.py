@@ -261,22 +261,35 @@ def test_bad_arguments_raise(ctx):
         ctx.upload(c["raw"], "q4_k", 256 + 64, 128)      # Q4_K needs in % 256 == 0
 
 
-def test_smem_and_cache_paths_agree_bitwise(ctx):
-    """Both operand paths round the same exact f32 dequantized value once to f16 and run the same
-    MMA sequence, so their forward outputs match bit for bit."""
+@pytest.mark.parametrize("tmem", [0, 1])
+def test_dequant_and_cache_paths_agree(ctx, tmem):
+    """Every operand path rounds the same exact f32 dequantized value once to f16.  The in-kernel
+    dequantization into a shared-memory B tile (tmem 0) runs the cache path's MMA sequence, so the
+    forward matches it bit for bit; with the weight as the tensor-memory operand (tmem 1) the
+    product is computed transposed, so only the f32 accumulation order differs."""
     import torch
     import sa3k
-    c = _case("q4_k", 300, 512, 768, 16, 21)
-    outs = []
-    for smem in (0, 1):
-        ctx.set_option(sa3k.OPT_SMEM_DEQUANT, smem)
-        w = ctx.upload(c["raw"], "q4_k", 512, 768)
-        y = torch.empty(300, 768, device="cuda")
-        ctx.linear_fwd(w, _dev(c["x"]), y)
-        ctx.sync()
-        outs.append(y.cpu().numpy())
+    outs = {}
+    for qtype, S, inn, out in (("q4_k", 300, 512, 768), ("q8_0", 260, 384, 200)):
+        c = _case(qtype, S, inn, out, 16, 21)
+        for smem in (0, 1):
+            ctx.set_option(sa3k.OPT_SMEM_DEQUANT, smem)
+            ctx.set_option(sa3k.OPT_DEQUANT_TMEM, tmem)
+            w = ctx.upload(c["raw"], qtype, inn, out)
+            y = torch.empty(S, out, device="cuda")
+            dx = torch.empty(S, inn, device="cuda")
+            ctx.linear_fwd(w, _dev(c["x"]), y)
+            ctx.linear_bwd(w, _dev(c["x"]), y, _dev(c["dy"]), dx)
+            ctx.sync()
+            outs[(qtype, smem)] = (y.cpu().numpy(), dx.cpu().numpy())
     ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
-    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    ctx.set_option(sa3k.OPT_DEQUANT_TMEM, 1)
+    for qtype in ("q4_k", "q8_0"):
+        for a, b in zip(outs[(qtype, 0)], outs[(qtype, 1)]):
+            if tmem == 0:
+                assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), qtype
+            else:
+                assert rel_l2(b, a) < 1e-6, (qtype, rel_l2(b, a))
 
 
 def test_linear_step_replays_from_cuda_graph(ctx):
