@@ -16,13 +16,13 @@
 // dequant warps), about 50 KB, where dequantizing into a shared-memory f16 B tile moves about
 // 130 KB for the same MMA work (codes in and out, f16 tile in and out, activation in and out).
 //
-// Warp roles (448 threads):
+// Warp roles (704 threads):
 //   warp 0        TMA producer: the activation tile [128 t][64 k] f16 (128B swizzle), the
 //                 codes [128 f][64 k] (64B swizzle; Q4_K: 32 bytes, 32B swizzle) and the
 //                 stage's block scales; for the K = 16 extension the u^T tile [16][128 t]
 //   warp 1        TMEM owner and MMA issue (A from TMEM, B from shared memory)
 //   warps 2-5     epilogue: one warp per TMEM lane quarter, all 128 token columns
-//   warps 6-13    dequant: two warps per lane quarter, 32 of the 64 k of a stage each, from
+//   warps 6-21    dequant: four warps per lane quarter, 32 of the 128 k of a stage each, from
 //                 the stage's codes in shared memory (conflict-free 16-byte reads)
 //
 // Tensor memory (512 columns): two 128-column accumulators and ASTAGES A stages of 32 columns
@@ -71,7 +71,7 @@ struct WqSmem {
   static_assert(DYN <= 232448, "shared memory budget (227 KB)");
 };
 
-constexpr int kWqEpiWarps = 4, kWqDqWarps = 8;
+constexpr int kWqEpiWarps = 4, kWqDqWarps = 16;
 constexpr int kWqThreads = 32 * (2 + kWqEpiWarps + kWqDqWarps);
 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
@@ -398,66 +398,58 @@ __global__ void __launch_bounds__(kWqThreads, 1)
             tmem_st8(dst, rr);
           }
         } else {
-          // codes of row r, k 64h .. 64h + 63 (rows beyond N and k beyond K read TMA's zero fill)
+          // codes of row r, k 32h .. 32h + 31 (rows beyond N and k beyond K read TMA's zero fill)
           const uint8_t* cst = smem + L::OFF_C + s * L::C_BYTES;
-          uint4 cw[4];
+          uint4 ca, cb = make_uint4(0, 0, 0, 0);
           if (QT == 0) {   // 128-byte rows, 128B swizzle: 16-byte chunk c at c ^ (r & 7)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              cw[j] = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((4 * h + j) ^ (r & 7)));
+            ca = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h) ^ (r & 7)));
+            cb = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h + 1) ^ (r & 7)));
           } else {         // 64-byte rows, 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
-#pragma unroll
-            for (int j = 0; j < 2; ++j)
-              cw[j] = *reinterpret_cast<const uint4*>(cst + r * 64 + 16 * ((2 * h + j) ^ ((r >> 1) & 3)));
-            cw[2] = cw[3] = make_uint4(0, 0, 0, 0);
+            ca = *reinterpret_cast<const uint4*>(cst + r * 64 + 16 * (h ^ ((r >> 1) & 3)));
           }
           const uint8_t* sc = smem + L::OFF_SC + s * L::SC_BYTES;
-          uint32_t rg[32];
+          uint32_t rg[16];
           if (args.nt) {
-            // one block scale per 32 k: scales [4 k-blocks][128 f], blocks 2h and 2h + 1
+            // one block scale for the 32 k: scales [4 k-blocks][128 f], block h
+            if (QT == 0) {
+              const float d = reinterpret_cast<const float*>(sc)[h * 128 + r];
+              const uint32_t dd = h2bits(d, d);   // exact: d is an f16 value
+              const uint4 c0 = q8_chunk_h(make_uint2(ca.x, ca.y), dd, dd, dd, dd);
+              const uint4 c1 = q8_chunk_h(make_uint2(ca.z, ca.w), dd, dd, dd, dd);
+              const uint4 c2 = q8_chunk_h(make_uint2(cb.x, cb.y), dd, dd, dd, dd);
+              const uint4 c3 = q8_chunk_h(make_uint2(cb.z, cb.w), dd, dd, dd, dd);
+              const uint32_t t16[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w,
+                                        c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
 #pragma unroll
-            for (int bq = 0; bq < 2; ++bq) {
-              if (QT == 0) {
-                const float d = reinterpret_cast<const float*>(sc)[(2 * h + bq) * 128 + r];
-                const uint32_t dd = h2bits(d, d);   // exact: d is an f16 value
-                const uint4 c0 = q8_chunk_h(make_uint2(cw[2 * bq].x, cw[2 * bq].y), dd, dd, dd, dd);
-                const uint4 c1 = q8_chunk_h(make_uint2(cw[2 * bq].z, cw[2 * bq].w), dd, dd, dd, dd);
-                const uint4 c2 = q8_chunk_h(make_uint2(cw[2 * bq + 1].x, cw[2 * bq + 1].y), dd, dd, dd, dd);
-                const uint4 c3 = q8_chunk_h(make_uint2(cw[2 * bq + 1].z, cw[2 * bq + 1].w), dd, dd, dd, dd);
-                const uint32_t t16[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w,
-                                          c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+              for (int j2 = 0; j2 < 16; ++j2) rg[j2] = t16[j2];
+            } else {
+              const float2 dm = reinterpret_cast<const float2*>(sc)[h * 128 + r];
+              const uint64_t d4[4] = {f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x)};
+              const uint64_t m4[4] = {f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y)};
+              const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
 #pragma unroll
-                for (int j2 = 0; j2 < 16; ++j2) rg[16 * bq + j2] = t16[j2];
-              } else {
-                const float2 dm = reinterpret_cast<const float2*>(sc)[(2 * h + bq) * 128 + r];
-                const uint64_t d4[4] = {f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x)};
-                const uint64_t m4[4] = {f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y)};
-                const uint32_t words[4] = {cw[bq].x, cw[bq].y, cw[bq].z, cw[bq].w};
-#pragma unroll
-                for (int w4 = 0; w4 < 4; ++w4) {
-                  const uint4 o = q4_chunk4(words[w4], d4, m4);
-                  rg[16 * bq + 4 * w4] = o.x; rg[16 * bq + 4 * w4 + 1] = o.y;
-                  rg[16 * bq + 4 * w4 + 2] = o.z; rg[16 * bq + 4 * w4 + 3] = o.w;
-                }
+              for (int w4 = 0; w4 < 4; ++w4) {
+                const uint4 o = q4_chunk4(words[w4], d4, m4);
+                rg[4 * w4] = o.x; rg[4 * w4 + 1] = o.y; rg[4 * w4 + 2] = o.z; rg[4 * w4 + 3] = o.w;
               }
             }
           } else {
             // the scale changes with k (k = the weight's output row): scales [4 f-blocks][128 k]
             if (QT == 0) {
-              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 32 + h * 16;   // 64 floats
+              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 32 + h * 8;   // 32 floats
+              const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
 #pragma unroll
-              for (int g = 0; g < 8; ++g) {   // 8 k per group: two float4 of scales
+              for (int g = 0; g < 4; ++g) {   // 8 k per group: two float4 of scales
                 const float4 s0 = sq[2 * g], s1 = sq[2 * g + 1];
-                const uint4 cc = cw[g >> 1];
-                const uint2 wv = (g & 1) ? make_uint2(cc.z, cc.w) : make_uint2(cc.x, cc.y);
-                const uint4 o = q8_chunk_h(wv, h2bits(s0.x, s0.y), h2bits(s0.z, s0.w), h2bits(s1.x, s1.y),
-                                           h2bits(s1.z, s1.w));
+                const uint4 o = q8_chunk_h(make_uint2(wv[2 * g], wv[2 * g + 1]), h2bits(s0.x, s0.y),
+                                           h2bits(s0.z, s0.w), h2bits(s1.x, s1.y), h2bits(s1.z, s1.w));
                 rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
               }
             } else {
-              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 64 + h * 32;   // 64 float2
+              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 64 + h * 16;   // 32 float2
+              const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
 #pragma unroll
-              for (int g = 0; g < 8; ++g) {   // 8 k: four float4 = (d0, m0, d1, m1) pairs
+              for (int g = 0; g < 4; ++g) {   // 8 k: four float4 = (d0, m0, d1, m1) pairs
                 uint64_t d4[4], m4[4];
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
@@ -465,14 +457,12 @@ __global__ void __launch_bounds__(kWqThreads, 1)
                   d4[p] = f2(dm.x, dm.z);
                   m4[p] = f2(-dm.y, -dm.w);
                 }
-                const uint4 cc = cw[g >> 2];
-                const uint32_t word = (g & 3) == 0 ? cc.x : (g & 3) == 1 ? cc.y : (g & 3) == 2 ? cc.z : cc.w;
-                const uint4 o = q4_chunk4(word, d4, m4);
+                const uint4 o = q4_chunk4(words[g], d4, m4);
                 rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
               }
             }
           }
-          tmem_st32_w(dst + (uint32_t)(32 * h), rg);
+          tmem_st16_w(dst + (uint32_t)(16 * h), rg);
         }
         tmem_st_wait_w();
         tc_fence_before();
