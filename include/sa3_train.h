@@ -214,8 +214,10 @@ struct TrainConditioning {
     int token_count = 0;
 };
 
-// src/train_inpaint.h:145-150.  Accepted by the step signature; the local-conditioning input is
-// not built on the device, so a non-null inpaint is refused with an error.
+// src/train_inpaint.h:145-150: local [frames][local_dim] (the frame mask, then the masked latent)
+// and loss_weight [frames][io] (build_train_inpaint).  A graph built with inpaint = true takes them
+// every step: the local-add conditioning runs in every block on the device and the loss is the
+// weighted sum.  Adapters on the local.* projections themselves are refused (the core scope).
 enum class InpaintMaskType { Segments, FullMask, Causal, Spans };
 struct TrainInpaint {
     std::vector<float> local;
@@ -230,6 +232,7 @@ struct TrainInpaint {
 struct TrainDitCkpt {
     void* pctx = nullptr;
     std::shared_ptr<DitDevice> device;
+    bool inpaint = false;
     int frames = 0, cond_dim = 0, ctx_len = 0;
 };
 

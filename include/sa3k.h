@@ -430,6 +430,18 @@ int sa3k_dit_forward_backward(sa3k_dit* dit, int B, int T, int ctx_len, const fl
                               const float* target, const float* t_feat, const float* cross,
                               const float* global, float* loss, char* err, int err_len);
 
+/* The same step with the inpaint objective (run_train_dit_accumulate_ckpt with a TrainInpaint,
+ * src/train_loop.h:309-313, src/train_inpaint.h:145-201): local [B][T][local_dim] is the
+ * local-add conditioning (build_train_inpaint: the frame mask, then the masked latent), added in
+ * every block after the cross-attention as local.2(silu(local.0(local))) to the T real tokens
+ * (src/dit.h:244-254); loss_weight [B][T][io] weights the squared error, loss[b] =
+ * sum(w (v - target)^2) (src/train_ckpt.h:369).  The model needs dit.local_dim > 0; adapters on the
+ * local.* projections themselves are refused (train the core scope).  Runs eagerly. */
+int sa3k_dit_forward_backward_inpaint(sa3k_dit* dit, int B, int T, int ctx_len, const float* x_t,
+                                      const float* target, const float* t_feat, const float* cross,
+                                      const float* global, const float* local, const float* loss_weight,
+                                      float* loss, char* err, int err_len);
+
 /* ---- adapter and trainer-state files (the reference's GGUF formats) ----
  * Adapter file (write_train_lora_gguf / load_train_lora_gguf, src/train_checkpoint.h:42-173):
  * metadata general.architecture "sa3-lora", lora.adapter_type, lora.rank, lora.alpha,

@@ -507,6 +507,77 @@ def mat_weight_torch(W, p, adapter_type, scale):
     return (rms(rowed.t(), out) * p["m_c"][:, None]).t()
 
 
+# --------------------------------------------------------------------------------------------
+# mode (ii): the activation rounding of ggml's CPU matrix multiply over a quantized weight
+# --------------------------------------------------------------------------------------------
+# In ggml's published design the CPU mul_mat converts the activation operand to the weight type's
+# vec_dot_type before the dot products: Q8_0 weights take Q8_0 activation blocks (32 values, an
+# f16 scale d = max|x| / 127, q = round(x / d)), Q4_K weights take Q8_K blocks (256 values, an f32
+# scale from the signed element of largest magnitude, iscale = -127 / max, q = min(127,
+# round(iscale x)), d = 1 / iscale); F16 weights take f16 activations.  The backward (OUT_PROD)
+# reads the f32-dequantized weight and is not rounded.  The ggml source is not available here, so
+# these two quantizers are restated from that design (the Q8_0 one is checked bit for bit against
+# gguf-py's, which states it matches ggml): "unverified" in the sense of the reference's own code.
+ACT_QUANT = {}   # weight name -> "q8_0" | "q8_k" | "f16": set by ggml_cpu_numerics()
+
+
+def act_round_q8_0(x):
+    """Q8_0 quantize + dequantize along the last dim (blocks of 32), float64 numpy."""
+    x = np.asarray(x, np.float64)
+    b = x.reshape(-1, 32).astype(np.float32)
+    d = np.abs(b).max(axis=1, keepdims=True) / np.float32(127)
+    with np.errstate(divide="ignore"):
+        idv = np.where(d == 0, 0, 1 / d).astype(np.float32)
+    q = np.sign(b * idv) * np.floor(np.abs(b * idv) + np.float32(0.5))   # roundf: half away from zero
+    dh = d.astype(np.float16).astype(np.float64)
+    return (q.astype(np.float64) * dh).reshape(x.shape)
+
+
+def act_round_q8_k(x):
+    """Q8_K quantize + dequantize along the last dim (blocks of 256), float64 numpy."""
+    x = np.asarray(x, np.float64)
+    b = x.reshape(-1, 256).astype(np.float32)
+    idx = np.abs(b).argmax(axis=1)
+    mx = b[np.arange(b.shape[0]), idx][:, None]
+    out = np.zeros_like(b, dtype=np.float64)
+    nz = (mx != 0)[:, 0]
+    iscale = (np.float32(-127.0) / mx[nz]).astype(np.float32)
+    v = iscale * b[nz]
+    q = np.minimum(np.float32(127), np.sign(v) * np.floor(np.abs(v) + np.float32(0.5)))
+    out[nz] = q.astype(np.float64) * (np.float32(1.0) / iscale).astype(np.float64)
+    return out.reshape(x.shape)
+
+
+class ggml_cpu_numerics:
+    """Context manager: within it, lin() rounds the activation of every base-weight product whose
+    weight name is in `qtypes` (name -> "q8_0" | "q4_k" | "f16") the way ggml's CPU backend would."""
+
+    def __init__(self, qtypes):
+        self.map = {n: {"q8_0": "q8_0", "q4_k": "q8_k", "f16": "f16"}[t] for n, t in qtypes.items()}
+
+    def __enter__(self):
+        ACT_QUANT.clear()
+        ACT_QUANT.update(self.map)
+        return self
+
+    def __exit__(self, *a):
+        ACT_QUANT.clear()
+
+
+def _act_round_ste(x, kind):
+    """The rounded activation forward, the identity backward (OUT_PROD does not see the rounding)."""
+    torch = _torch()
+    xd = x.detach().cpu().numpy()
+    if kind == "q8_0":
+        r = act_round_q8_0(xd)
+    elif kind == "q8_k":
+        r = act_round_q8_k(xd)
+    else:
+        r = xd.astype(np.float16).astype(np.float64)
+    r = torch.tensor(r, dtype=x.dtype, device=x.device)
+    return x + (r - x).detach()
+
+
 def lin(Wd, lora, name, x, bias=None):
     """dit_lin over torch tensors: Wd[name] is W[out][in]; lora[name] = dict(A,B,m,bns,scale), or
     for a materialized family dict(type, scale, A, B | U, V, M, m | m_r, m_c): x W_eff^T, the
@@ -517,7 +588,8 @@ def lin(Wd, lora, name, x, bias=None):
     if p is not None and p.get("type"):
         y = torch.matmul(x, mat_weight_torch(W, p, p["type"], p["scale"]).t())
         return y + bias if bias is not None else y
-    y = torch.matmul(x, W.t())
+    xb = _act_round_ste(x, ACT_QUANT[name]) if name in ACT_QUANT else x
+    y = torch.matmul(xb, W.t())
     if p is not None:
         A, B, s = p["A"], p["B"], p["scale"]
         y = y + s * torch.matmul(torch.matmul(x, A.t()), B.t())
@@ -532,8 +604,9 @@ def lin(Wd, lora, name, x, bias=None):
     return y
 
 
-def dit_block(Wd, lora, pfx, x, context, gcond, pos, c: DitCfg, window=None):
-    """src/dit.h:164-266 for one sample: x[S][dim], context[Ctx][dim], gcond[6*dim]."""
+def dit_block(Wd, lora, pfx, x, context, gcond, pos, c: DitCfg, window=None, local=None):
+    """src/dit.h:164-266 for one sample: x[S][dim], context[Ctx][dim], gcond[6*dim]; local
+    [T][local_dim] (inpaint local conditioning, src/dit.h:244-254) or None."""
     torch = _torch()
     dim, hd, nh = c.dim, c.head_dim, c.heads
     S, Ctx = x.shape[0], context.shape[0]
@@ -584,6 +657,11 @@ def dit_block(Wd, lora, pfx, x, context, gcond, pos, c: DitCfg, window=None):
         oc = attn(cq, ck, cv, None)
     oc = lin(Wd, lora, pfx + "cross.out.weight", oc)
     x = x + oc
+    if local is not None:
+        # local.0 -> SiLU -> local.2, added to the T real tokens (the memory tokens get + 0)
+        le = silu(lin(Wd, lora, pfx + "local.0.weight", local, Wd[pfx + "local.0.bias"]))
+        le = lin(Wd, lora, pfx + "local.2.weight", le, Wd[pfx + "local.2.bias"])
+        x = torch.cat([x[:c.mem_tokens], x[c.mem_tokens:] + le], 0)
 
     res = x
     f = rms_norm(x, Wd[pfx + "ff_norm.gamma"], c.norm_eps) * (1.0 + sc_f) + sh_f
@@ -618,17 +696,43 @@ def dit_tail(Wd, lora, x, c: DitCfg):
     return lin(Wd, lora, "dit.post_conv.weight", x) + x
 
 
-def dit_loss(Wd, lora, x_t, t_feat, cross, glob, target, c: DitCfg, window=None):
-    """One sample's loss: mean((v - target)^2) over io*frames (src/train_ckpt.h:226-228)."""
+def dit_loss(Wd, lora, x_t, t_feat, cross, glob, target, c: DitCfg, window=None, local=None, loss_weight=None):
+    """One sample's loss: mean((v - target)^2) over io*frames (src/train_ckpt.h:226-228); with an
+    inpaint input, sum(loss_weight * (v - target)^2) (src/train_ckpt.h:369, the weights of
+    build_train_inpaint, src/train_inpaint.h:165-201) and the local conditioning in every block."""
     torch = _torch()
     x0, context, gcond = dit_head(Wd, lora, x_t, t_feat, cross, glob, c)
     pos = torch.arange(x0.shape[0])
     x = x0
     for l in range(c.depth):
-        x = dit_block(Wd, lora, f"dit.{l}.", x, context, gcond, pos, c, window)
+        x = dit_block(Wd, lora, f"dit.{l}.", x, context, gcond, pos, c, window, local)
     vel = dit_tail(Wd, lora, x, c)
     d = vel - target
+    if loss_weight is not None:
+        return (loss_weight * d * d).sum()
     return (d * d).sum() / (c.io * target.shape[0])
+
+
+def inpaint_inputs(z, mask, io, local_dim, mask_loss_weight=1.0, mask_padding_attention=True):
+    """The local conditioning [T][local_dim] and loss weight [T][io] of build_train_inpaint
+    (src/train_inpaint.h:165-201): channel 0 the frame mask, channels 1..io the masked latent;
+    weights 1 / (io n_gen) on generated frames and 0 on context frames (mask_padding_attention),
+    else normalised with mask_loss_weight on the context frames."""
+    z = np.asarray(z, np.float32)
+    T = z.shape[0]
+    local = np.zeros((T, local_dim), np.float32)
+    local[:, 0] = mask
+    local[:, 1:1 + io] = z * mask[:, None]
+    n_ctx = int(np.sum(mask > 0.5))
+    n_gen = T - n_ctx
+    f = np.float32
+    if mask_padding_attention:
+        wg, wc = f(1.0) / (f(io) * f(n_gen) + f(1e-8)), f(0.0)
+    else:
+        den = f(io) * f(n_gen) + f(mask_loss_weight) * f(io) * f(n_ctx) + f(1e-8)
+        wg, wc = f(1.0) / den, f(mask_loss_weight) / den
+    w = np.where(mask[:, None] > 0.5, wc, wg).astype(np.float32) * np.ones((1, io), np.float32)
+    return local, w
 
 
 # --------------------------------------------------------------------------------------------

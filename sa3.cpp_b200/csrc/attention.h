@@ -110,9 +110,14 @@ int k_mod_grad_gate(Ctx* c, const float* gy, const float* y, const float* gate, 
                     long out_stride, float* dgate, std::string& err);
 int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err);
 
-// loss[b] = sum((vel - target)^2) / (io*T) per sample; dvel = grad_scale * 2 (vel - target) / (io*T)
+// loss[b] = sum((vel - target)^2) / (io*T) per sample; dvel = grad_scale * 2 (vel - target) / (io*T);
+// with weight (nullable, [B][io*T]): loss[b] = sum(w (vel - target)^2), dvel = grad_scale * 2 w (vel - target)
 int k_mse(Ctx* c, const float* vel, const float* target, int B, long per_sample, float* loss, float* dvel,
-          float grad_scale, std::string& err);
+          float grad_scale, const float* weight, std::string& err);
+// dst[r][c] = c < w ? f16(src[r][c]) : 0, rows of ld (>= w) f16
+int k_pad_f16(Ctx* c, const float* src, long rows, int w, __half* dst, long ld, std::string& err);
+// rows t >= mem of each sample (S rows) get le's row of that real token added: dst = y + le (dst may be y)
+int k_add_local(Ctx* c, const float* y, const float* le, int B, int S, int mem, int D, float* dst, std::string& err);
 // x *= s over n floats (in place)
 int k_scale(Ctx* c, float* x, long n, float s, std::string& err);
 

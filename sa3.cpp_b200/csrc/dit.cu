@@ -98,6 +98,15 @@ struct DitModel {
   // not tile (dit.local_dim = 257); [out][in] f32 with their (in, out)
   std::map<std::string, std::vector<float>> host_w;
   std::map<std::string, std::pair<int64_t, int64_t>> host_shape;
+  // the same weights zero-padded to a multiple of 64 in `in` on the device: the inpaint local.0
+  // projection of the local-conditioning input, run by the GEMM engine (name -> padded weight)
+  std::map<std::string, Weight*> Wpad;
+  // inpaint: the current call carries a local-conditioning input and loss weights
+  // (sa3k_dit_forward_backward_inpaint); local_ld = dit.local_dim rounded up to 64
+  bool inpaint = false;
+  int64_t local_ld = 0;
+  float *in_local = nullptr, *in_lw = nullptr, *lmid = nullptr;
+  __half *local_h = nullptr, *lmid_h = nullptr;
   std::vector<void*> owned;            // device allocations of this model
   // adapters
   bool dora = false;
@@ -382,6 +391,11 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     m.loss = f(64); m.dp = f(MT * k.io); m.dxT = f(MT * D);
     const int64_t wide = std::max<int64_t>(std::max<int64_t>(Q, 2 * I), D);
     m.gx = f(M * D); m.dtmp = f(M * wide); m.dh = f(M * D); m.dact_b = h(M * I); m.dq3 = f(M * Q);
+    if (k.local_dim > 0) {   // inpaint local conditioning (used only by the calls that carry it)
+      m.local_ld = ((int64_t)k.local_dim + 63) / 64 * 64;
+      m.in_local = f(MT * k.local_dim); m.in_lw = f(MT * k.io); m.lmid = f(MT * D);
+      m.local_h = h(MT * m.local_ld); m.lmid_h = h(MT * D);
+    }
     m.Dsum = f(B * Hh * S); m.dO_b = h(M * D);
     m.dv2 = diff ? f(M * D) : nullptr;
     m.pre_lin = f(MT * k.io); m.vel_lin = f(MT * k.io); m.g_y = f(B * D); m.ctx_y = f(MC * D);
@@ -592,6 +606,7 @@ static int dit_step(DitModel& m, std::string& err) {
   // 1 / gscale after it: both exact in f32, the accumulated gradients come out unscaled.
   const float gscale = std::exp2(std::floor(std::log2(0.5f * (float)T * (float)k.io)));
   if (m.np > 0 && k_scale(c, m.g, m.np, gscale, err)) return 1;
+  if (m.inpaint && k_pad_f16(c, m.in_local, MT, k.local_dim, m.local_h, m.local_ld, err)) return 1;
 
   // adapters: operand forms + DoRA norms, once per step (grouped launches over all adapters; the
   // DoRA P = W A^T GEMMs run per adapter between them)
@@ -721,8 +736,23 @@ static int dit_step(DitModel& m, std::string& err) {
       if (k_sub_f16(c, a.oc1, a.oc2, M * D, a.oc, err)) return 1;
     }
     if (lin_fwd(m, wco, tco, nullptr, a.oc, M, tco ? a.yc : m.dtmp, nullptr, err)) return 1;
+    if (m.inpaint) {
+      // inpaint local conditioning (src/dit.h:244-254): local.2(silu(local.0(local))) added to
+      // the T real tokens of every sample, the memory tokens + 0; the local.* projections are
+      // frozen and the input is data, so nothing of this branch is differentiated
+      const Weight* wl0 = m.Wpad.count(m.bname(l, "local.0.weight")) ? m.Wpad[m.bname(l, "local.0.weight")]
+                                                                      : m.weight(m.bname(l, "local.0.weight"), err);
+      const Weight* wl2 = m.weight(m.bname(l, "local.2.weight"), err);
+      const float* bl0 = m.vec(m.bname(l, "local.0.bias"), err);
+      const float* bl2 = m.vec(m.bname(l, "local.2.bias"), err);
+      if (!wl0 || !wl2 || !bl0 || !bl2) return 1;
+      if (lin_fwd(m, wl0, nullptr, bl0, m.local_h, MT, m.lmid, nullptr, err)) return 1;
+      if (k_silu_f16(c, m.lmid, (long)MT * D, m.lmid_h, err)) return 1;
+      if (lin_fwd(m, wl2, nullptr, bl2, m.lmid_h, MT, m.lmid, nullptr, err)) return 1;
+      if (k_add_local(c, tco ? a.yc : m.dtmp, m.lmid, B, S, k.mem_tokens, D, m.dtmp, err)) return 1;
+    }
     // x2 = x1 + cross-attention output, then the feed-forward branch's modulated norm of x2
-    if (k_residual_norm(c, a.x1, tco ? a.yc : m.dtmp, nullptr, 0, (int)M, D, S, a.x2, g_ff, a.mod + 3 * D,
+    if (k_residual_norm(c, a.x1, (tco && !m.inpaint) ? a.yc : m.dtmp, nullptr, 0, (int)M, D, S, a.x2, g_ff, a.mod + 3 * D,
                         a.mod + 4 * D, ms, k.norm_eps, a.hf, a.rstd_f, err))
       return 1;
     if (lin_fwd(m, wfp, tp, b_fp, a.hf, M, nullptr, a.ff, err)) return 1;
@@ -750,7 +780,8 @@ static int dit_step(DitModel& m, std::string& err) {
   if (lin_fwd(m, wpo, tpo, nullptr, m.xT_b, MT, m.pout, m.pout_b, err)) return 1;
   if (lin_fwd(m, wpc, tpc, nullptr, m.pout_b, MT, m.vel_lin, nullptr, err)) return 1;
   if (k_add(c, m.vel_lin, m.pout, (long)MT * k.io, m.vel, err)) return 1;
-  if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, gscale, err)) return 1;
+  if (k_mse(c, m.vel, m.in_target, B, (long)T * k.io, m.loss, m.dvel, gscale, m.inpaint ? m.in_lw : nullptr, err))
+    return 1;
 
   // ---------------- backward
   if (cudaMemcpyAsync(m.dp, m.dvel, sizeof(float) * MT * k.io, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
@@ -1126,6 +1157,15 @@ int sa3k_dit_set_tensor(sa3k_dit* d, const char* name, int type, const void* hos
       const __half* hh = static_cast<const __half*>(host);
       for (size_t i = 0; i < v.size(); ++i) v[i] = __half2float(hh[i]);
     }
+    // a device copy zero-padded to a multiple of 64 in `in` for the GEMM engine (the padding
+    // meets zero columns of the padded input: the products are those of the logical weight)
+    const int64_t ld = (ne0 + 63) / 64 * 64;
+    std::vector<float> pad((size_t)(ld * ne1), 0.0f);
+    for (int64_t o = 0; o < ne1; ++o) std::memcpy(&pad[(size_t)(o * ld)], &v[(size_t)(o * ne0)], 4 * (size_t)ne0);
+    sa3k_weight* hp = nullptr;
+    if (sa3k_weight_upload(m.handle, SA3K_TYPE_F32, pad.data(), ld, ne1, &hp, err, err_len)) return 1;
+    m.weights.push_back(hp);
+    m.Wpad[n] = &hp->w;
     m.host_w[n] = std::move(v);
     m.host_shape[n] = {ne0, ne1};
     return 0;
@@ -1411,6 +1451,39 @@ int sa3k_dit_forward_backward(sa3k_dit* d, int B, int T, int ctx_len, const floa
   if (loss && cudaMemcpyAsync(loss, m.loss, sizeof(float) * B, cudaMemcpyDefault, st) != cudaSuccess)
     return dfail(err, err_len, "loss copy failed");
   return 0;
+}
+
+int sa3k_dit_forward_backward_inpaint(sa3k_dit* d, int B, int T, int ctx_len, const float* x_t, const float* target,
+                                      const float* t_feat, const float* cross, const float* global,
+                                      const float* local, const float* loss_weight, float* loss, char* err,
+                                      int err_len) {
+  if (!d || !local || !loss_weight) return dfail(err, err_len, "NULL argument");
+  DitModel& m = d->m;
+  const sa3k_dit_config& k = m.cfg;
+  if (k.local_dim <= 0)
+    return dfail(err, err_len, "inpainting requested but the DiT has no local-cond weights (dit.local_dim <= 0)");
+  for (const DitTarget& t : m.tg)
+    if (t.name.find(".local.") != std::string::npos)
+      return dfail(err, err_len, "adapters on the local.* projections are not trained with an inpaint input here "
+                                 "(the core scope leaves them out): " + t.name);
+  if (m.tg.empty()) return dfail(err, err_len, "no adapters: call sa3k_dit_init_adapters first");
+  if (B <= 0 || B > 64 || T <= 0 || ctx_len <= 0) return dfail(err, err_len, "bad batch shape");
+  cudaSetDevice(m.c->device);
+  std::string e;
+  if (alloc_acts(m, B, T, ctx_len, e)) return dfail(err, err_len, e);
+  const int64_t MT = (int64_t)B * T;
+  const cudaStream_t st = m.c->stream;
+  if (cudaMemcpyAsync(m.in_local, local, sizeof(float) * MT * k.local_dim, cudaMemcpyDefault, st) != cudaSuccess ||
+      cudaMemcpyAsync(m.in_lw, loss_weight, sizeof(float) * MT * k.io, cudaMemcpyDefault, st) != cudaSuccess)
+    return dfail(err, err_len, "input copy failed");
+  // the inpaint step runs eagerly (the recorded step graph is the plain one)
+  const bool graph = m.c->step_graph;
+  m.c->step_graph = false;
+  m.inpaint = true;
+  const int rc = sa3k_dit_forward_backward(d, B, T, ctx_len, x_t, target, t_feat, cross, global, loss, err, err_len);
+  m.inpaint = false;
+  m.c->step_graph = graph;
+  return rc;
 }
 
 int sa3k_dit_apply_adamw(sa3k_dit* d, int count, const sa3k_adamw_params* hp, int step, double* grad_norm_out,

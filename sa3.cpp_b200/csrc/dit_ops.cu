@@ -608,16 +608,21 @@ __global__ void modulation_kernel(const float* __restrict__ ssg, const float* __
   }
 }
 
-__global__ void mse_kernel(const float* __restrict__ vel, const float* __restrict__ tgt, long per, float inv,
-                           float gscale, float* __restrict__ loss, float* __restrict__ dvel) {
+__global__ void mse_kernel(const float* __restrict__ vel, const float* __restrict__ tgt, const float* __restrict__ wt,
+                           long per, float inv, float gscale, float* __restrict__ loss, float* __restrict__ dvel) {
   pdl_prologue();
   const int b = blockIdx.y;
   float acc = 0.f;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < per; i += (long)gridDim.x * blockDim.x) {
     const long e = (long)b * per + i;
     const float d = vel[e] - tgt[e];
-    acc += d * d;
-    if (dvel) dvel[e] = 2.f * d * inv * gscale;
+    if (wt) {   // inpaint: sum of w (v - t)^2, the weights carry the normalisation
+      acc += wt[e] * d * d;
+      if (dvel) dvel[e] = 2.f * wt[e] * d * gscale;
+    } else {
+      acc += d * d;
+      if (dvel) dvel[e] = 2.f * d * inv * gscale;
+    }
   }
   acc = warp_sum(acc);
   __shared__ float part[32];
@@ -626,7 +631,34 @@ __global__ void mse_kernel(const float* __restrict__ vel, const float* __restric
   if (threadIdx.x < 32) {
     float v = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
     v = warp_sum(v);
-    if (threadIdx.x == 0) atomicAdd(loss + b, v * inv);
+    if (threadIdx.x == 0) atomicAdd(loss + b, wt ? v : v * inv);
+  }
+}
+
+// dst[r][c] = c < w ? f16(src[r][c]) : 0 for c < ld (a row-padded f16 copy)
+__global__ void pad_f16_kernel(const float* __restrict__ src, long rows, int w, __half* __restrict__ dst, long ld) {
+  pdl_prologue();
+  const long n = rows * ld;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / ld;
+    const int cc = (int)(i - r * ld);
+    dst[i] = __float2half_rn(cc < w ? src[r * w + cc] : 0.f);
+  }
+}
+
+// dst[b S + t][:] = y[b S + t][:] + (t >= mem ? le[b (S - mem) + t - mem][:] : 0); dst may be y
+__global__ void add_local_kernel(const float* y, const float* __restrict__ le, long rows, int S, int mem, int D,
+                                 float* dst) {
+  pdl_prologue();
+  const long n = rows * D;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / D;
+    const int col = (int)(i - r * D);
+    const long b = r / S;
+    const int t = (int)(r - b * S);
+    float v = y[i];
+    if (t >= mem) v += le[(b * (S - mem) + (t - mem)) * D + col];
+    dst[i] = v;
   }
 }
 
@@ -860,12 +892,24 @@ int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, flo
 }
 
 int k_mse(Ctx* c, const float* vel, const float* target, int B, long per, float* loss, float* dvel, float grad_scale,
-          std::string& err) {
+          const float* weight, std::string& err) {
   ProfScope prof_(c, "mse");
   if (cudaMemsetAsync(loss, 0, sizeof(float) * B, c->stream) != cudaSuccess) return check_launch("mse memset", err);
   dim3 grid(16, (unsigned)B);
-  launch_pdl(c, mse_kernel, grid, 256, 0, vel, target, per, 1.0f / (float)per, grad_scale, loss, dvel);
+  launch_pdl(c, mse_kernel, grid, 256, 0, vel, target, weight, per, 1.0f / (float)per, grad_scale, loss, dvel);
   return check_launch("mse", err);
+}
+
+int k_pad_f16(Ctx* c, const float* src, long rows, int w, __half* dst, long ld, std::string& err) {
+  ProfScope prof_(c, "pad_f16");
+  launch_pdl(c, pad_f16_kernel, gs(rows * ld), 256, 0, src, rows, w, dst, ld);
+  return check_launch("pad_f16", err);
+}
+
+int k_add_local(Ctx* c, const float* y, const float* le, int B, int S, int mem, int D, float* dst, std::string& err) {
+  ProfScope prof_(c, "add_local");
+  launch_pdl(c, add_local_kernel, gs((long)B * S * D), 256, 0, y, le, (long)B * S, S, mem, D, dst);
+  return check_launch("add_local", err);
 }
 
 int k_scale(Ctx* c, float* x, long n, float s, std::string& err) {

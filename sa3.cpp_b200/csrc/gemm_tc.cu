@@ -341,7 +341,13 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   // and the context has not asked for the in-smem path explicitly
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
                      !(d.w->f16 && !c->smem_dequant);
-  if (quant && c->dequant_tmem && wq_fits(d)) return gemm_wq(c, d, err);
+  if (quant && c->dequant_tmem && wq_fits(d)) {
+    // (inside a stream capture the transposed codes of an input-gradient GEMM cannot be made: such
+    // a GEMM keeps to the shared-memory dequant path until an eager call has made them)
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool capturing = cudaStreamIsCapturing(c->stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+    if (d.bsrc == kB_WEIGHT_NT || d.w->codes_t || !capturing) return gemm_wq(c, d, err);
+  }
   int bn = d.bn;
   if (bn == 128) bn = c->tile_n ? c->tile_n : pick_bn(c, d.M, d.N, quant);
   if (quant && bn == 192) bn = 256;

@@ -521,7 +521,8 @@ bool TrainDiffusionSampler::restore_state(const std::string& state, std::string&
 bool build_train_dit_ckpt(GgufModel& dit, const DitConfig& dc, const TrainLoraState& lora, int frames, int cond_dim,
                           int ctx_len, TrainDitCkpt& out, std::string& err, bool inpaint) {
     if (frames <= 0 || cond_dim <= 0 || ctx_len <= 0) return fail(err, "invalid DiT training graph dimensions");
-    if (inpaint) return fail(err, "the inpaint local-conditioning input is not built on this device path");
+    if (inpaint && dc.local_dim <= 0)
+        return fail(err, "inpainting requested but DiT has no local-cond weights (dit.local_dim <= 0)");
     if (!dit.backend) return fail(err, "the model has no backend (load_gguf(path, backend))");
     if (cond_dim != dc.cond_dim) return fail(err, "cond_dim does not match the model");
     std::vector<std::string> names;
@@ -575,6 +576,7 @@ bool build_train_dit_ckpt(GgufModel& dit, const DitConfig& dc, const TrainLoraSt
     }
     out.device = dev;
     out.pctx = dev.get();
+    out.inpaint = inpaint;
     out.frames = frames;
     out.cond_dim = cond_dim;
     out.ctx_len = ctx_len;
@@ -593,8 +595,9 @@ bool run_train_dit_accumulate_ckpt(Backend backend, TrainDitCkpt& ck, const Trai
                                    std::string& err, const TrainInpaint* inpaint) {
     if (sample.x_t.empty() || sample.velocity_target.empty() || cond.cross.empty() || cond.global.empty())
         return fail(err, "training step inputs are empty");
-    if (inpaint) return fail(err, "inpaint graph/sample mismatch (local-cond present in one but not the other)");
     if (!device_alive(ck.device, err)) return false;
+    if (ck.inpaint != (inpaint != nullptr))
+        return fail(err, "inpaint graph/sample mismatch (local-cond present in one but not the other)");
     DitDevice& d = *ck.device;
     if (backend && backend != d.ctx) return fail(err, "backend differs from the one the graph was built on");
     const int64_t T = (int64_t)sample.x_t.size() / dc.io;
@@ -611,10 +614,21 @@ bool run_train_dit_accumulate_ckpt(Backend backend, TrainDitCkpt& ck, const Trai
     std::vector<float> tf;
     expo_features(sample.t, tf, dc.time_dim, dc.time_min_freq, dc.time_max_freq);
     float loss = 0.f;
-    if (!ok_or(sa3k_dit_forward_backward(d.dit, 1, (int)T, ck.ctx_len, sample.x_t.data(), sample.velocity_target.data(),
-                                         tf.data(), cond.cross.data(), cond.global.data(), &loss, e, kErrLen),
-               e, err))
+    if (inpaint) {
+        if ((int64_t)inpaint->local.size() != T * dc.local_dim || (int64_t)inpaint->loss_weight.size() != T * dc.io)
+            return fail(err, "inpaint input size does not match the training graph");
+        if (!ok_or(sa3k_dit_forward_backward_inpaint(d.dit, 1, (int)T, ck.ctx_len, sample.x_t.data(),
+                                                     sample.velocity_target.data(), tf.data(), cond.cross.data(),
+                                                     cond.global.data(), inpaint->local.data(),
+                                                     inpaint->loss_weight.data(), &loss, e, kErrLen),
+                   e, err))
+            return false;
+    } else if (!ok_or(sa3k_dit_forward_backward(d.dit, 1, (int)T, ck.ctx_len, sample.x_t.data(),
+                                                sample.velocity_target.data(), tf.data(), cond.cross.data(),
+                                                cond.global.data(), &loss, e, kErrLen),
+                      e, err)) {
         return false;
+    }
     if (!ok_or(sa3k_sync(d.ctx, e, kErrLen), e, err)) return false;
     // this sample's gradients into the host accumulator
     d.stage.assign((size_t)d.np, 0.f);

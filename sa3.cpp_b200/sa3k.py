@@ -24,7 +24,7 @@ ABI_SYMBOLS = (
     "sa3k_attention_fwd", "sa3k_attention_bwd", "sa3k_attention_bwd_noalloc", "sa3k_head_prep_fwd", "sa3k_head_prep_bwd",
     "sa3k_dit_create", "sa3k_dit_free", "sa3k_dit_set_tensor", "sa3k_dit_init_adapters", "sa3k_dit_adapter_size",
     "sa3k_dit_adapter_offsets", "sa3k_dit_adapter_buffer", "sa3k_dit_adapter_copy", "sa3k_dit_zero_grads",
-    "sa3k_dit_forward_backward", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create", "sa3k_dp_comm_create_timeout",
+    "sa3k_dit_forward_backward", "sa3k_dit_forward_backward_inpaint", "sa3k_dit_apply_adamw", "sa3k_dp_unique_id", "sa3k_dp_comm_create", "sa3k_dp_comm_create_timeout",
     "sa3k_dp_comm_destroy", "sa3k_dp_comm_info", "sa3k_dp_allreduce_sum", "sa3k_dp_allreduce_adamw",
     "sa3k_dit_dp_apply_adamw", "sa3k_dit_save_adapter", "sa3k_dit_load_adapter", "sa3k_dit_save_checkpoint",
     "sa3k_dit_load_checkpoint", "sa3k_adapter_gguf_write", "sa3k_gguf_get_string", "sa3k_gguf_get_u64",
@@ -557,6 +557,13 @@ class Dit:
         err = ctypes.create_string_buffer(1024)
         _check(lib().sa3k_dit_forward_backward(self._h, B, T, ctx_len, _ptr(x_t), _ptr(target), _ptr(t_feat),
                                                _ptr(cross), _ptr(glob), _ptr(loss), err, 1024), err)
+
+    def forward_backward_inpaint(self, B, T, ctx_len, x_t, target, t_feat, cross, glob, local, loss_weight, loss=None):
+        """forward_backward with the inpaint local conditioning [B][T][local_dim] and loss weights [B][T][io]."""
+        err = ctypes.create_string_buffer(1024)
+        _check(lib().sa3k_dit_forward_backward_inpaint(self._h, B, T, ctx_len, _ptr(x_t), _ptr(target), _ptr(t_feat),
+                                                       _ptr(cross), _ptr(glob), _ptr(local), _ptr(loss_weight),
+                                                       _ptr(loss), err, 1024), err)
 
     def dp_apply_adamw(self, comm, samples_per_rank, hp, step, want_norm=False):
         """All-reduce the gradients over comm's ranks, then AdamW with count = samples_per_rank x ranks."""

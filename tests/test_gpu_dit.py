@@ -246,3 +246,66 @@ def test_step_in_kernel_dequant_matches_cache(ctx, differential):
     ctx.set_option(sa3k.OPT_SMEM_DEQUANT, 0)
     np.testing.assert_allclose(res[1][0], res[0][0], rtol=1e-5)
     assert rel_l2(res[1][1], res[0][1]) < 1e-4
+
+
+@pytest.mark.parametrize("padding_attention", [True, False])
+def test_dit_step_inpaint_matches_oracle(ctx, padding_attention):
+    """The inpaint objective (src/train_inpaint.h:165-201, src/dit.h:244-254): a model with the
+    local.* projections (local_dim 65, zero-padded to 128 for the GEMM engine), the local-add
+    conditioning of a random frame mask in every block, and the weighted loss; loss and every
+    adapter gradient against float64 autograd.  Adapters on the local.* projections are refused."""
+    import sa3k
+    cfg = dict(CFG, local_dim=65)
+    dit, deq, ad, targets, rng = _build(ctx, cfg, scope="config4")
+    x_t, target, tfeat, cross, glob = _inputs(rng)
+    z = rng.standard_normal((B, T, CFG["io"])).astype(np.float32)
+    locals_, weights = [], []
+    for b in range(B):
+        mask = (rng.uniform(0, 1, T) < 0.4).astype(np.float32)
+        lc, w = oracle.inpaint_inputs(z[b], mask, CFG["io"], 65, mask_loss_weight=0.5,
+                                      mask_padding_attention=padding_attention)
+        locals_.append(lc)
+        weights.append(w)
+    local = np.stack(locals_)
+    lw = np.stack(weights)
+    dit.zero_grads()
+    loss = np.zeros(B, np.float32)
+    dit.forward_backward_inpaint(B, T, CTX, x_t, target, tfeat, cross, glob, local, lw, loss=loss)
+    ctx.sync()
+    grads = np.zeros(dit.size(), np.float32)
+    dit.copy(1, grads, to_model=False)
+
+    import torch
+    c = oracle.DitCfg(io=cfg["io"], dim=cfg["dim"], depth=cfg["depth"], heads=cfg["heads"], cond_dim=cfg["cond_dim"],
+                      mem_tokens=cfg["mem_tokens"], rot=cfg["rot"], time_dim=cfg["time_dim"], ff_inner=cfg["ff_inner"])
+    T64 = lambda a: torch.tensor(np.asarray(a, np.float64))
+    Wd = {k: T64(v) for k, v in deq.items()}
+    lora, leaves = {}, {}
+    for name, p in ad.items():
+        A, Bm, m = (T64(p[k]).requires_grad_(True) for k in ("A", "B", "m"))
+        bns, _ = oracle.row_norms(deq[name])
+        lora[name] = dict(A=A, B=Bm, m=m, bns=T64(bns), scale=ALPHA / RANK)
+        leaves[name] = (A, Bm, m)
+    ref_loss = []
+    for b in range(B):
+        lb = oracle.dit_loss(Wd, lora, T64(x_t[b]), T64(tfeat[b]), T64(cross[b]), T64(glob[b]), T64(target[b]), c,
+                             local=T64(local[b]), loss_weight=T64(lw[b]))
+        lb.backward()
+        ref_loss.append(float(lb.detach()))
+    np.testing.assert_allclose(loss, ref_loss, rtol=1e-3)
+    worst = {}
+    for name in targets:
+        oa, ob, om = ad[name]["offs"]
+        for lab, off, t in zip(("dA", "dB", "dm"), (oa, ob, om), leaves[name]):
+            r = t.grad.numpy()
+            worst[f"{name}:{lab}"] = rel_l2(grads[off:off + r.size].reshape(r.shape), r)
+    top = sorted(((v, k) for k, v in worst.items()), reverse=True)[:4]
+    print(f"[inpaint padding_attention={padding_attention}] worst:", "; ".join(f"{k} {v:.3g}" for v, k in top))
+    bad = sorted((v, k) for k, v in worst.items() if not v < 1e-2)
+    assert not bad, bad
+    dit.close()
+
+    full, _, _, _, _ = _build(ctx, cfg, scope="full")
+    with pytest.raises(sa3k.Sa3kError, match="local"):
+        full.forward_backward_inpaint(B, T, CTX, x_t, target, tfeat, cross, glob, local, lw)
+    full.close()

@@ -167,3 +167,36 @@ def test_dit_step_config4_widths(ctx, differential):
         oa, ob, om = ad[name]["offs"]
         for off, n in ((oa, ad[name]["A"].size), (ob, ad[name]["B"].size), (om, ad[name]["m"].size)):
             assert rel_l2(p1[off:off + n], rp[off:off + n]) < TOL_GRAD, name
+
+
+def test_distance_to_ggml_cpu_numerics(ctx):
+    """Reported, not gated: how far the GPU step's adapter gradients lie from the oracle in mode (ii),
+    the activation rounding of ggml's CPU backend over a Q8_0 base (every frozen linear's input
+    rounded to Q8_0 blocks before its forward product), next to how far mode (ii) lies from the
+    exact step.  The best available estimate of the distance to the reference's own CPU path,
+    whose ggml kernels are not available to run."""
+    cfg = dict(CFG)
+    dit, deq, ad, targets, rng = _build(ctx, cfg, seed=21)
+    inputs = _inputs(rng, cfg)
+    dit.zero_grads()
+    loss = np.zeros(B, np.float32)
+    dit.forward_backward(B, T, CTX, *inputs, loss=loss)
+    ctx.sync()
+    grads = np.zeros(dit.size(), np.float32)
+    dit.copy(1, grads, to_model=False)
+    dit.close()
+    _, exact = _reference(cfg, deq, ad, inputs)
+    qnames = {n: "q8_0" for n in deq if n.endswith(".weight")}
+    with oracle.ggml_cpu_numerics(qnames):
+        ref2_loss, mode2 = _reference(cfg, deq, ad, inputs)
+    gpu_m2, ex_m2 = [], []
+    for name in targets:
+        oa, ob, om = ad[name]["offs"]
+        for k, off in enumerate((oa, ob, om)):
+            r2 = mode2[name][k].ravel()
+            gpu_m2.append(rel_l2(grads[off:off + r2.size], r2))
+            ex_m2.append(rel_l2(exact[name][k].ravel(), r2))
+    print(f"\n[mode ii] gradient rel-L2 GPU vs ggml-CPU numerics: median {np.median(gpu_m2):.3g} max {max(gpu_m2):.3g}; "
+          f"exact vs ggml-CPU numerics: median {np.median(ex_m2):.3g} max {max(ex_m2):.3g}; "
+          f"loss GPU {loss.tolist()} mode-ii {ref2_loss.tolist()}")
+    assert np.all(np.isfinite(gpu_m2)) and np.all(np.isfinite(ex_m2))
