@@ -46,7 +46,7 @@ def _worker(rank, world, port, outdir):
     comm = None
     try:
         ctx = sa3k.Context(rank)
-        dit, _, _, _, _ = base._build(ctx, seed=0)               # same base + adapters on every rank
+        dit, _, _, _, _ = base._build(ctx, dict(base.CFG), seed=0)   # same base + adapters on every rank
         uid = dp.exchange_unique_id(rank, sa3k.dp_unique_id, dist.broadcast_object_list)
         comm = sa3k.DpComm(ctx, world, rank, uid)
         tr = dp.DataParallelTrainer(dit, dp.NcclReduce(comm))
@@ -81,7 +81,7 @@ def test_two_gpu_dp_step_matches_one_gpu(ctx):
         r0, r1 = np.load(os.path.join(d, "r0.npz")), np.load(os.path.join(d, "r1.npz"))
     assert np.array_equal(r0["p"], r1["p"]), "ranks disagree after the all-reduce + AdamW"
 
-    dit, _, _, _, _ = base._build(ctx, seed=0)
+    dit, _, _, _, _ = base._build(ctx, dict(base.CFG), seed=0)
     p0 = np.zeros(dit.size(), np.float32)
     dit.copy(0, p0, to_model=False)
     tr = dp.DataParallelTrainer(dit)
