@@ -10,7 +10,7 @@ weights and inputs.  Unit: samples/s summed over all ranks.
 
 Reported beside the device-timed value: the GEMM engine's roofline (algorithmic FLOPs / its summed
 CUDA-event time inside a replayed graph, against the measured bf16 peak), the same GEMMs through
-the in-smem Q8_0 dequant path, the e2e value through the C ABI with pinned host inputs, a CPU
+the in-kernel Q8_0 dequant path (codes dequantized into tensor memory), the e2e value through the C ABI with pinned host inputs, a CPU
 restatement baseline, nvidia-smi clocks sampled during the timed region and the launch count.
 
 --workload linear: BASELINE configs[1] (one DoRA Q4_K 1536 -> 6144 linear, 2048 tokens) as a
@@ -354,14 +354,14 @@ def main_linear(args):
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": WORKLOAD, "global_batch": world, "seq_len": S, "parallelism": f"dp{world}",
                        "l2": "256 MB flush between timed steps"},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": traffic,
-                         "kernel": "linear.fwd + linear.dx: tcgen05 GEMM on the bf16 copy of the Q4_K "
-                                   "base (dequantized once, bit-exact, at upload)",
-                         "peak_kind": f"{peak_kind} bf16 burst", "launches": n_gemm,
+                         "kernel": "linear.fwd + linear.dx: tcgen05 GEMM on the f16 copy of the Q4_K "
+                                   "base (dequantized once, each value rounded once to f16, at upload)",
+                         "peak_kind": f"{peak_kind} bf16 burst (f16 runs at the same tensor rate)", "launches": n_gemm,
                          "kernel_ms_per_step": ms_gemm / args.steps},
             "quant_gemm_smem_dequant": {
                 "bound": "tensor", "achieved": achieved_q, "peak": peak_tf, "unit": "TFLOP/s",
@@ -532,8 +532,8 @@ class DitCpuStep:
         return dt
 
 
-def dit_cpu_sample_note(threads):
-    return (f"whole samples of the config-4 step (head, 24 blocks, tail, MSE loss, backward to all 96 DoRA "
+def dit_cpu_sample_note(threads, one=False):
+    return (f"{'one whole sample' if one else 'whole samples'} of the config-4 step (head, 24 blocks, tail, MSE loss, backward to all 96 DoRA "
             f"adapters; 1088 tokens, cross 128x768), float32 torch CPU restatement of the reference's math "
             f"(oracle.dit_loss) on {threads} threads, weights built before timing (the blocks share one block's "
             f"frozen tensors; adapters per block), the first sample untimed "
@@ -574,7 +574,7 @@ def run_dit_reference(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": dit_config_line(args, cfg),
             "cpu_baseline": {"value": value, "unit": "samples/s", "cores": os.cpu_count(), "kind": "port",
-                             "sample": "each step: one " + dit_cpu_sample_note(os.cpu_count())},
+                             "sample": "each step: " + dit_cpu_sample_note(os.cpu_count(), one=True)},
             "e2e": {"value": value, "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -756,13 +756,13 @@ def main_dit(args):
         line = {
             "metric": METRIC, "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": dit_config_line(args, cfg),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "traffic": None,
                          "kernel": "tcgen05 GEMM engine, classes linear.fwd + linear.dx (all frozen-base "
-                                   "projections of the step; Q8_0 base via its bf16 operand copy)",
-                         "peak_kind": f"{peak_kind} bf16 burst",
+                                   "projections of the step; Q8_0 base via its f16 operand copy)",
+                         "peak_kind": f"{peak_kind} bf16 burst (f16 runs at the same tensor rate)",
                          "kernel_ms_per_step": ms_gemm / kprof, "algorithmic_tflop_per_step": gflops / 1e12},
             "quant_gemm_smem_dequant": {
                 "achieved": achieved_q, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved_q / peak_tf,
@@ -1090,7 +1090,7 @@ KERNEL_CASES = ("gemm", "attn-dit", "mat")
 
 
 def main():
-    ap = argparse.ArgumentParser()
+    ap = argparse.ArgumentParser(allow_abbrev=False)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)

@@ -133,8 +133,9 @@ static int launch(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const CUtens
   a.kb_per_split = nkb > 0 ? nkb : 1;
   a.partial = nullptr;
   // (splits that end in the in-kernel reduction keep >= 16 k-blocks each: below that the
-  // reduction by the last CTA of a tile costs more than the shorter K loop saves)
-  const int min_kb = (d.atomic_split && d.out && !d.out_h) ? 4 : 16;
+  // reduction by the last CTA of a tile costs more than the shorter K loop saves; a 16-wide
+  // tile's reduction reads only 8 KB a split, so the rank-16 GEMMs split down to 4 k-blocks)
+  const int min_kb = ((d.atomic_split && d.out && !d.out_h) || BN == 16) ? 4 : 16;
   if (tiles * 2 <= (long)c->sm_count && nkb >= 2 * min_kb) {
     int splits = (int)((long)c->sm_count / tiles);
     if (splits > nkb / min_kb) splits = nkb / min_kb;

@@ -11,22 +11,25 @@
 //
 // Why this form: a tcgen05 MMA reads its B operand from shared memory but may take A from tensor
 // memory.  Dequantizing the weight straight into tensor memory (registers -> tcgen05.st) keeps the
-// f16 weight tile out of shared memory: per 64-k step the shared-memory traffic is the activation
-// tile (written by TMA, read by the MMA) plus the 1-byte codes (written by TMA, read once by the
-// dequant warps), about 50 KB, where dequantizing into a shared-memory f16 B tile moves about
-// 130 KB for the same MMA work (codes in and out, f16 tile in and out, activation in and out).
+// f16 weight tile out of shared memory: per 128-k stage the shared-memory traffic is the
+// activation tile (32 KB, written by TMA, read by the MMA) plus the 1-byte codes and the scales
+// (18 KB, written by TMA, read once by the dequant warps), where dequantizing into a shared-memory
+// f16 operand tile would add 64 KB of f16 writes and reads for the same MMA work.
 //
-// Warp roles (704 threads):
-//   warp 0        TMA producer: the activation tile [128 t][64 k] f16 (128B swizzle), the
-//                 codes [128 f][64 k] (64B swizzle; Q4_K: 32 bytes, 32B swizzle) and the
-//                 stage's block scales; for the K = 16 extension the u^T tile [16][128 t]
-//   warp 1        TMEM owner and MMA issue (A from TMEM, B from shared memory)
+// Warp roles (736 threads) and their three rings:
+//   warp 0        activation producer (X ring, kWqXStages): the tile [128 t][128 k] f16 as two
+//                 128B-swizzled 64-k halves; for the K = 16 extension the u^T tile [16][128 t].
+//                 A slot is freed by the MMA that read it.
+//   warp 1        TMEM owner and MMA issue (A from TMEM, B from shared memory), 8 MMAs a stage
 //   warps 2-5     epilogue: one warp per TMEM lane quarter, all 128 token columns
 //   warps 6-21    dequant: four warps per lane quarter, 32 of the 128 k of a stage each, from
-//                 the stage's codes in shared memory (conflict-free 16-byte reads)
+//                 the codes ring into the A ring (kWqAStages, tensor memory; freed by the MMA)
+//   warp 22       codes producer (C ring, kWqCStages): codes [128 f][128 k] (128B swizzle; Q4_K
+//                 64 bytes a row, 64B swizzle) and the stage's block scales.  A slot is freed by
+//                 the dequant warps once they hold its values, so the codes run ahead of the MMA.
 //
-// Tensor memory (512 columns): two 128-column accumulators and ASTAGES A stages of 32 columns
-// (64 f16 per lane).  The dequantized value is the exact f32 product of the reference's
+// Tensor memory (512 columns): two 128-column accumulators and kWqAStages A stages of 64 columns
+// (128 f16 per lane).  The dequantized value is the exact f32 product of the reference's
 // dequantization rounded once to f16 -- the same value the f16 operand cache holds.
 #pragma once
 
@@ -55,7 +58,7 @@ struct WqArgs {
   int* err;
 };
 
-constexpr int kWqF = 128, kWqT = 128, kWqK = 128, kWqXStages = 4, kWqAStages = 4;
+constexpr int kWqF = 128, kWqT = 128, kWqK = 128, kWqXStages = 4, kWqAStages = 4, kWqCStages = 5;
 
 template <int QT>
 struct WqSmem {
@@ -64,15 +67,16 @@ struct WqSmem {
   static constexpr int SC_BYTES = (QT == 0 ? 4 : 8) * 512;         // 4 x 128 scales (f32 or float2)
   static constexpr int OFF_X = 0;
   static constexpr int OFF_C = OFF_X + kWqXStages * X_BYTES;
-  static constexpr int OFF_SC = OFF_C + kWqXStages * C_BYTES;
-  static constexpr int OFF_BAR = OFF_SC + kWqXStages * SC_BYTES;
-  static constexpr int BAR_BYTES = (2 * kWqXStages + 2 * kWqAStages + 4) * 8 + 16;
+  static constexpr int OFF_SC = OFF_C + kWqCStages * C_BYTES;
+  static constexpr int OFF_BAR = OFF_SC + kWqCStages * SC_BYTES;
+  static constexpr int BAR_BYTES = (2 * kWqXStages + 2 * kWqAStages + 2 * kWqCStages + 4) * 8 + 16;
   static constexpr int DYN = OFF_BAR + BAR_BYTES + 1024;
   static_assert(DYN <= 232448, "shared memory budget (227 KB)");
 };
 
 constexpr int kWqEpiWarps = 4, kWqDqWarps = 16;
-constexpr int kWqThreads = 32 * (2 + kWqEpiWarps + kWqDqWarps);
+constexpr int kWqCodeWarp = 2 + kWqEpiWarps + kWqDqWarps;   // the codes / scales producer
+constexpr int kWqThreads = 32 * (kWqCodeWarp + 1);
 
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile(
@@ -162,6 +166,128 @@ __device__ __forceinline__ uint32_t h2bits(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+// Dequantize this thread's part of a stage into 16 packed f16 pairs: row r of the 128-feature
+// tile (quarter q = r / 32) and k 32h .. 32h + 31 of the stage, from the stage's codes cst and
+// block scales sc in shared memory (TMA layouts: codes 128B-swizzled rows, Q4_K 64B-swizzled).
+template <int QT>
+__device__ __forceinline__ void wq_dequant(const uint8_t* cst, const uint8_t* sc, bool nt, int r, int q, int h,
+                                           uint32_t (&rg)[16]) {
+  // codes of row r, k 32h .. 32h + 31 (rows beyond N and k beyond K read TMA's zero fill)
+  uint4 ca, cb = make_uint4(0, 0, 0, 0);
+  if (QT == 0) {   // 128-byte rows, 128B swizzle: 16-byte chunk c at c ^ (r & 7)
+    ca = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h) ^ (r & 7)));
+    cb = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h + 1) ^ (r & 7)));
+  } else {         // 64-byte rows, 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
+    ca = *reinterpret_cast<const uint4*>(cst + r * 64 + 16 * (h ^ ((r >> 1) & 3)));
+  }
+  if (nt) {
+    // one block scale for the 32 k: scales [4 k-blocks][128 f], block h
+    if (QT == 0) {
+      const float d = reinterpret_cast<const float*>(sc)[h * 128 + r];
+      const uint32_t dd = h2bits(d, d);   // exact: d is an f16 value
+      const uint4 c0 = q8_chunk_h(make_uint2(ca.x, ca.y), dd, dd, dd, dd);
+      const uint4 c1 = q8_chunk_h(make_uint2(ca.z, ca.w), dd, dd, dd, dd);
+      const uint4 c2 = q8_chunk_h(make_uint2(cb.x, cb.y), dd, dd, dd, dd);
+      const uint4 c3 = q8_chunk_h(make_uint2(cb.z, cb.w), dd, dd, dd, dd);
+      const uint32_t t16[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w,
+                                c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
+#pragma unroll
+      for (int j2 = 0; j2 < 16; ++j2) rg[j2] = t16[j2];
+    } else {
+      const float2 dm = reinterpret_cast<const float2*>(sc)[h * 128 + r];
+      const uint64_t d4[4] = {f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x)};
+      const uint64_t m4[4] = {f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y)};
+      const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
+#pragma unroll
+      for (int w4 = 0; w4 < 4; ++w4) {
+        const uint4 o = q4_chunk4(words[w4], d4, m4);
+        rg[4 * w4] = o.x; rg[4 * w4 + 1] = o.y; rg[4 * w4 + 2] = o.z; rg[4 * w4 + 3] = o.w;
+      }
+    }
+  } else {
+    // the scale changes with k (k = the weight's output row): scales [4 f-blocks][128 k]
+    if (QT == 0) {
+      const float4* sq = reinterpret_cast<const float4*>(sc) + q * 32 + h * 8;   // 32 floats
+      const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {   // 8 k per group: two float4 of scales
+        const float4 s0 = sq[2 * g], s1 = sq[2 * g + 1];
+        const uint4 o = q8_chunk_h(make_uint2(wv[2 * g], wv[2 * g + 1]), h2bits(s0.x, s0.y),
+                                   h2bits(s0.z, s0.w), h2bits(s1.x, s1.y), h2bits(s1.z, s1.w));
+        rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
+      }
+    } else {
+      const float4* sq = reinterpret_cast<const float4*>(sc) + q * 64 + h * 16;   // 32 float2
+      const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {   // 8 k: four float4 = (d0, m0, d1, m1) pairs
+        uint64_t d4[4], m4[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const float4 dm = sq[4 * g + p];
+          d4[p] = f2(dm.x, dm.z);
+          m4[p] = f2(-dm.y, -dm.w);
+        }
+        const uint4 o = q4_chunk4(words[g], d4, m4);
+        rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
+      }
+    }
+  }
+}
+
+// Epilogue of one accumulator: lane = feature f (TMEM lane), the tile's kWqT token columns from
+// tacc; out = alpha * col_scale[f] * acc + col_bias[f] into the outputs args names.  `have` false
+// (an aborted tile): the TMEM reads still run (warp-aligned), nothing is stored.
+__device__ __forceinline__ void wq_drain(const WqArgs& args, uint32_t tacc, int f, int t0, bool have) {
+  const bool fin = f < args.N;
+  float cs = args.alpha, cb = 0.f;
+  if (fin && args.col_scale) cs *= args.col_scale[f];
+  if (fin && args.col_bias) cb = args.col_bias[f];
+#pragma unroll 1
+  for (int c0 = 0; c0 < kWqT; c0 += 32) {
+    uint32_t v[32];
+    tmem_ld32(tacc + (uint32_t)c0, v);
+    tmem_ld_wait();
+    if (!have || !fin) continue;
+    const int tb = t0 + c0;
+    float x[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * cs + cb;
+    if (args.out && !args.out_trans) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (tb + j >= args.M) break;
+        float* dst = args.out + (long)(tb + j) * args.ldo + f;
+        *dst = args.accumulate ? *dst + x[j] : x[j];
+      }
+    }
+    if (args.out && args.out_trans) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (tb + j >= args.M) break;
+        float* dst = args.out + (long)f * args.ldo + tb + j;
+        *dst = args.accumulate ? *dst + x[j] : x[j];
+      }
+    }
+    if (args.out_h) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (tb + j >= args.M) break;
+        const __half hv = __float2half_rn(x[j] * args.h_scale);
+        if (args.out_h_trans) args.out_h[(long)f * args.ldo_h + tb + j] = hv;
+        else args.out_h[(long)(tb + j) * args.ldo_h + f] = hv;
+      }
+    }
+    if (args.out_h_t) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (tb + j >= args.M) break;
+        args.out_h_t[(long)f * args.ldo_h_t + tb + j] = __float2half_rn(x[j]);
+      }
+    }
+  }
+}
+
 template <int QT>
 __global__ void __launch_bounds__(kWqThreads, 1)
     gemm_wq_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c,
@@ -176,7 +302,9 @@ __global__ void __launch_bounds__(kWqThreads, 1)
   uint64_t* xempty = xfull + kWqXStages;
   uint64_t* afull = xempty + kWqXStages;
   uint64_t* aempty = afull + kWqAStages;
-  uint64_t* tfull = aempty + kWqAStages;   // [2]
+  uint64_t* cfull = aempty + kWqAStages;
+  uint64_t* cempty = cfull + kWqCStages;
+  uint64_t* tfull = cempty + kWqCStages;   // [2]
   uint64_t* tempty = tfull + 2;            // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -196,6 +324,10 @@ __global__ void __launch_bounds__(kWqThreads, 1)
     for (int s = 0; s < kWqAStages; ++s) {
       mbar_init(&afull[s], 32 * kWqDqWarps);
       mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < kWqCStages; ++s) {
+      mbar_init(&cfull[s], 1);
+      mbar_init(&cempty[s], 32 * kWqDqWarps);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
@@ -244,20 +376,16 @@ __global__ void __launch_bounds__(kWqThreads, 1)
       int it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < ntiles && ok; item += gridDim.x) {
-        const int f0 = (item % tiles_f) * kWqF, t0 = (item / tiles_f) * kWqT;
+        const int t0 = (item / tiles_f) * kWqT;
         for (int kb = 0; kb < total; ++kb, ++it) {
           const int s = it % kWqXStages;
           const uint32_t use = (uint32_t)(it / kWqXStages);
           if (it >= kWqXStages && !wait(&xempty[s], (use & 1u) ^ 1u, kErrTimeoutEmpty)) { ok = false; break; }
           uint8_t* xs = smem + L::OFF_X + s * L::X_BYTES;
           if (kb < nkb) {
-            mbar_arrive_expect_tx(&xfull[s], (uint32_t)(L::X_BYTES + L::C_BYTES + L::SC_BYTES));
+            mbar_arrive_expect_tx(&xfull[s], (uint32_t)L::X_BYTES);
             tma_load_2d(xs, &tm_x, &xfull[s], kb * kWqK, t0);
             tma_load_2d(xs + L::X_BYTES / 2, &tm_x, &xfull[s], kb * kWqK + 64, t0);
-            tma_load_2d(smem + L::OFF_C + s * L::C_BYTES, &tm_c, &xfull[s], kb * kWqK / (QT == 0 ? 1 : 2), f0);
-            uint8_t* sc = smem + L::OFF_SC + s * L::SC_BYTES;
-            if (args.nt) tma_load_2d(sc, &tm_sc, &xfull[s], f0, kb * 4);        // [4 k-blocks][128 f]
-            else tma_load_2d(sc, &tm_sc, &xfull[s], kb * kWqK, f0 / 32);         // [4 f-blocks][128 k]
           } else {
             // extension: u^T rows t0 .. t0 + 127 as two MN-major 64 (t) x 16 (k) boxes
             mbar_arrive_expect_tx(&xfull[s], (uint32_t)(2 * 64 * 16 * 2));
@@ -314,57 +442,32 @@ __global__ void __launch_bounds__(kWqThreads, 1)
       const int a = ti & 1;
       const bool have = wait(&tfull[a], (uint32_t)(ti >> 1) & 1u, kErrTimeoutAccum);
       tc_fence_after();
-      const int f = f0 + 32 * q + lane;
-      const bool fin = f < args.N;
-      float cs = args.alpha, cb = 0.f;
-      if (fin && args.col_scale) cs *= args.col_scale[f];
-      if (fin && args.col_bias) cb = args.col_bias[f];
-      const uint32_t tacc = tbase + (uint32_t)(a * kWqT) + ((uint32_t)(32 * q) << 16);
-#pragma unroll 1
-      for (int c0 = 0; c0 < kWqT; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tacc + (uint32_t)c0, v);
-        tmem_ld_wait();
-        if (!have || !fin) continue;
-        const int tb = t0 + c0;
-        float x[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * cs + cb;
-        if (args.out && !args.out_trans) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (tb + j >= args.M) break;
-            float* dst = args.out + (long)(tb + j) * args.ldo + f;
-            *dst = args.accumulate ? *dst + x[j] : x[j];
-          }
-        }
-        if (args.out && args.out_trans) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (tb + j >= args.M) break;
-            float* dst = args.out + (long)f * args.ldo + tb + j;
-            *dst = args.accumulate ? *dst + x[j] : x[j];
-          }
-        }
-        if (args.out_h) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (tb + j >= args.M) break;
-            const __half hv = __float2half_rn(x[j] * args.h_scale);
-            if (args.out_h_trans) args.out_h[(long)f * args.ldo_h + tb + j] = hv;
-            else args.out_h[(long)(tb + j) * args.ldo_h + f] = hv;
-          }
-        }
-        if (args.out_h_t) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (tb + j >= args.M) break;
-            args.out_h_t[(long)f * args.ldo_h_t + tb + j] = __float2half_rn(x[j]);
-          }
-        }
-      }
+      wq_drain(args, tbase + (uint32_t)(a * kWqT) + ((uint32_t)(32 * q) << 16), f0 + 32 * q + lane, t0, have);
       tc_fence_before();
       mbar_arrive(&tempty[a]);
+    }
+  } else if (warp == kWqCodeWarp) {
+    // ------------------------------------------------------------ codes / scales producer
+    // Its ring is released by the dequant warps as soon as they hold a stage's values, not by
+    // the MMA: the codes run ahead of the activations by up to kWqCStages.
+    if (lane == 0) {
+      int ic = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < ntiles && ok; item += gridDim.x) {
+        const int f0 = (item % tiles_f) * kWqF;
+        for (int kb = 0; kb < nkb; ++kb, ++ic) {
+          const int s = ic % kWqCStages;
+          if (ic >= kWqCStages && !wait(&cempty[s], ((uint32_t)(ic / kWqCStages) & 1u) ^ 1u, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&cfull[s], (uint32_t)(L::C_BYTES + L::SC_BYTES));
+          tma_load_2d(smem + L::OFF_C + s * L::C_BYTES, &tm_c, &cfull[s], kb * kWqK / (QT == 0 ? 1 : 2), f0);
+          uint8_t* sc = smem + L::OFF_SC + s * L::SC_BYTES;
+          if (args.nt) tma_load_2d(sc, &tm_sc, &cfull[s], f0, kb * 4);        // [4 k-blocks][128 f]
+          else tma_load_2d(sc, &tm_sc, &cfull[s], kb * kWqK, f0 / 32);         // [4 f-blocks][128 k]
+        }
+      }
     }
   } else {
     // ------------------------------------------------------------ dequant into tensor memory
@@ -372,20 +475,34 @@ __global__ void __launch_bounds__(kWqThreads, 1)
     const int q = warp & 3, h = (warp - 2 - kWqEpiWarps) / 4;
     const int r = 32 * q + lane;
     const uint32_t lane_off = (uint32_t)(32 * q) << 16;
-    int it = 0;
+    int it = 0, ic = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < ntiles && ok; item += gridDim.x) {
       const int f = (item % tiles_f) * kWqF + r;
       for (int kb = 0; kb < total; ++kb, ++it) {
-        const int s = it % kWqXStages, as = it % kWqAStages;
-        uint4 ca = make_uint4(0, 0, 0, 0), cb = ca;
-        if (kb >= nkb && h == 0 && f < args.N) {   // extension: the 16 f16 of ext_b row f
-          const uint4* p = reinterpret_cast<const uint4*>(args.ext_b + (long)f * 64);
-          ca = __ldg(p);
-          cb = __ldg(p + 1);
+        const int as = it % kWqAStages;
+        uint32_t rg[16];
+        if (kb >= nkb) {
+          // extension: the 16 f16 of ext_b row f
+          uint4 ca = make_uint4(0, 0, 0, 0), cb = ca;
+          if (h == 0 && f < args.N) {
+            const uint4* p = reinterpret_cast<const uint4*>(args.ext_b + (long)f * 64);
+            ca = __ldg(p);
+            cb = __ldg(p + 1);
+          }
+          rg[0] = ca.x; rg[1] = ca.y; rg[2] = ca.z; rg[3] = ca.w;
+          rg[4] = cb.x; rg[5] = cb.y; rg[6] = cb.z; rg[7] = cb.w;
+        } else {
+          // the stage's codes and scales (TMA), dequantized into registers; each thread hands
+          // the slot back to the codes producer before it waits for a free A stage
+          const int cs = ic % kWqCStages;
+          if (!wait(&cfull[cs], (uint32_t)(ic / kWqCStages) & 1u, kErrTimeoutFull)) { ok = false; break; }
+          ++ic;
+          wq_dequant<QT>(smem + L::OFF_C + cs * L::C_BYTES, smem + L::OFF_SC + cs * L::SC_BYTES, args.nt != 0, r, q, h,
+                         rg);
+          mbar_arrive(&cempty[cs]);
         }
-        // the stage's codes and scales (TMA) and a free A stage (the MMA that read it is done)
-        if (!wait(&xfull[s], (uint32_t)(it / kWqXStages) & 1u, kErrTimeoutFull)) { ok = false; break; }
+        // a free A stage (the MMA that read it is done)
         if (it >= kWqAStages && !wait(&aempty[as], ((uint32_t)(it / kWqAStages) & 1u) ^ 1u, kErrTimeoutEmpty)) {
           ok = false;
           break;
@@ -394,74 +511,10 @@ __global__ void __launch_bounds__(kWqThreads, 1)
         const uint32_t dst = tA + (uint32_t)(as * (kWqK / 2)) + lane_off;
         if (kb >= nkb) {
           if (h == 0) {
-            const uint32_t rr[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+            const uint32_t rr[8] = {rg[0], rg[1], rg[2], rg[3], rg[4], rg[5], rg[6], rg[7]};
             tmem_st8(dst, rr);
           }
         } else {
-          // codes of row r, k 32h .. 32h + 31 (rows beyond N and k beyond K read TMA's zero fill)
-          const uint8_t* cst = smem + L::OFF_C + s * L::C_BYTES;
-          uint4 ca, cb = make_uint4(0, 0, 0, 0);
-          if (QT == 0) {   // 128-byte rows, 128B swizzle: 16-byte chunk c at c ^ (r & 7)
-            ca = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h) ^ (r & 7)));
-            cb = *reinterpret_cast<const uint4*>(cst + r * 128 + 16 * ((2 * h + 1) ^ (r & 7)));
-          } else {         // 64-byte rows, 64B swizzle: chunk c at c ^ ((r >> 1) & 3)
-            ca = *reinterpret_cast<const uint4*>(cst + r * 64 + 16 * (h ^ ((r >> 1) & 3)));
-          }
-          const uint8_t* sc = smem + L::OFF_SC + s * L::SC_BYTES;
-          uint32_t rg[16];
-          if (args.nt) {
-            // one block scale for the 32 k: scales [4 k-blocks][128 f], block h
-            if (QT == 0) {
-              const float d = reinterpret_cast<const float*>(sc)[h * 128 + r];
-              const uint32_t dd = h2bits(d, d);   // exact: d is an f16 value
-              const uint4 c0 = q8_chunk_h(make_uint2(ca.x, ca.y), dd, dd, dd, dd);
-              const uint4 c1 = q8_chunk_h(make_uint2(ca.z, ca.w), dd, dd, dd, dd);
-              const uint4 c2 = q8_chunk_h(make_uint2(cb.x, cb.y), dd, dd, dd, dd);
-              const uint4 c3 = q8_chunk_h(make_uint2(cb.z, cb.w), dd, dd, dd, dd);
-              const uint32_t t16[16] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w,
-                                        c2.x, c2.y, c2.z, c2.w, c3.x, c3.y, c3.z, c3.w};
-#pragma unroll
-              for (int j2 = 0; j2 < 16; ++j2) rg[j2] = t16[j2];
-            } else {
-              const float2 dm = reinterpret_cast<const float2*>(sc)[h * 128 + r];
-              const uint64_t d4[4] = {f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x), f2(dm.x, dm.x)};
-              const uint64_t m4[4] = {f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y), f2(-dm.y, -dm.y)};
-              const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
-#pragma unroll
-              for (int w4 = 0; w4 < 4; ++w4) {
-                const uint4 o = q4_chunk4(words[w4], d4, m4);
-                rg[4 * w4] = o.x; rg[4 * w4 + 1] = o.y; rg[4 * w4 + 2] = o.z; rg[4 * w4 + 3] = o.w;
-              }
-            }
-          } else {
-            // the scale changes with k (k = the weight's output row): scales [4 f-blocks][128 k]
-            if (QT == 0) {
-              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 32 + h * 8;   // 32 floats
-              const uint32_t wv[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
-#pragma unroll
-              for (int g = 0; g < 4; ++g) {   // 8 k per group: two float4 of scales
-                const float4 s0 = sq[2 * g], s1 = sq[2 * g + 1];
-                const uint4 o = q8_chunk_h(make_uint2(wv[2 * g], wv[2 * g + 1]), h2bits(s0.x, s0.y),
-                                           h2bits(s0.z, s0.w), h2bits(s1.x, s1.y), h2bits(s1.z, s1.w));
-                rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
-              }
-            } else {
-              const float4* sq = reinterpret_cast<const float4*>(sc) + q * 64 + h * 16;   // 32 float2
-              const uint32_t words[4] = {ca.x, ca.y, ca.z, ca.w};
-#pragma unroll
-              for (int g = 0; g < 4; ++g) {   // 8 k: four float4 = (d0, m0, d1, m1) pairs
-                uint64_t d4[4], m4[4];
-#pragma unroll
-                for (int p = 0; p < 4; ++p) {
-                  const float4 dm = sq[4 * g + p];
-                  d4[p] = f2(dm.x, dm.z);
-                  m4[p] = f2(-dm.y, -dm.w);
-                }
-                const uint4 o = q4_chunk4(words[g], d4, m4);
-                rg[4 * g] = o.x; rg[4 * g + 1] = o.y; rg[4 * g + 2] = o.z; rg[4 * g + 3] = o.w;
-              }
-            }
-          }
           tmem_st16_w(dst + (uint32_t)(16 * h), rg);
         }
         tmem_st_wait_w();

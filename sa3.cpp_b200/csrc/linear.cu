@@ -66,7 +66,10 @@ int adapter_prepare(Ctx* c, const Weight* w, AdapterPrep& p, std::string& err) {
 
 int lora_u(Ctx* c, const __half* x_h, int64_t M, int64_t in, const AdapterPrep& ad, __half* ut,
            int64_t ut_ld, std::string& err) {
-  GemmDesc g;   // u = x A^T  [M][16], written as ut = f16(u)^T [16][ut_ld]
+  // u = x A^T  [M][16], written as ut = f16(u)^T [16][ut_ld]: the HBM-shaped rank-16 kernel, or
+  // the GEMM engine for widths it does not take
+  if (in % 32 == 0) return k_r16_proj(c, x_h, (long)in, M, in, ad.a_h, 1.0f, ut, (long)ut_ld, "lora.u", err);
+  GemmDesc g;
   g.M = (int)M; g.N = 16; g.K = (int)in;
   g.a = x_h; g.lda = in;
   g.bsrc = kB_F16_KMAJOR; g.b = ad.a_h; g.ldb = in;
@@ -106,8 +109,10 @@ int linear_backward(Ctx* c, const LinearBwd& b, std::string& err) {
                        dora ? b.dg : nullptr, err))
       return 1;
   }
-  if (ad) {
-    GemmDesc g;   // du = s dz B  [M][16], written as dut = f16(du)^T [16][ut_ld]
+  if (ad && out % 32 == 0) {   // du = s dz B  [M][16], written as dut = f16(du)^T [16][ut_ld]
+    if (k_r16_proj(c, b.dz, (long)out, b.M, out, ad->bt_h, ad->s, b.dut, (long)b.ut_ld, "lora.du", err)) return 1;
+  } else if (ad) {
+    GemmDesc g;   // (the GEMM engine for widths the rank-16 kernel does not take)
     g.M = (int)b.M; g.N = 16; g.K = (int)out;
     g.a = b.dz; g.lda = out;
     g.bsrc = kB_F16_KMAJOR; g.b = ad->bt_h; g.ldb = out;

@@ -210,12 +210,28 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
 
 // SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (f16), da (f16)
 // the gradient of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I
-// columns).  Thread = 4 columns of val and the matching 4 of gate, block = kFuseTok rows (two
-// rows' loads first); dz = f16(g dy) and, for DoRA, dg += colsum(dy (y - bias) / g).
-__device__ __forceinline__ void f16x4(const uint2 w, float (&v)[4]) {
-  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w.x));
-  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w.y));
-  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+// columns).  Thread = 8 columns of val and the matching 8 of gate (16-byte loads and stores),
+// block = kFuseTok rows, kSwiRows rows' loads issued at a time; dz = f16(g dy) and, for DoRA,
+// dg += colsum(dy (y - bias) / g) with the reciprocals of g taken once per thread.
+constexpr int kSwiRows = 4;
+
+__device__ __forceinline__ void f16x8(const uint4 w, float (&v)[8]) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u[k]));
+    v[2 * k] = a.x;
+    v[2 * k + 1] = a.y;
+  }
+}
+
+__device__ __forceinline__ void f32x8(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ uint4 f16x8_pack(const float (&v)[8]) {
+  return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]));
 }
 
 __global__ void swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half* __restrict__ f, int T,
@@ -223,63 +239,64 @@ __global__ void swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half
                                      const float* __restrict__ bias, const float* __restrict__ g,
                                      __half* __restrict__ dz, float* __restrict__ dg) {
   pdl_prologue();
-  const int j = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  const int j = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
   const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
   const bool dora = g != nullptr;
-  float gvv[4] = {1.f, 1.f, 1.f, 1.f}, ggg[4] = {1.f, 1.f, 1.f, 1.f};
-  float bvv[4] = {0.f, 0.f, 0.f, 0.f}, bgg[4] = {0.f, 0.f, 0.f, 0.f};
+  float gv[8], gg[8], igv[8], igg[8], bv[8], bg[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) gv[e] = gg[e] = igv[e] = igg[e] = 1.f, bv[e] = bg[e] = 0.f;
   if (dora) {
-    const float4 a4 = *reinterpret_cast<const float4*>(g + j), b4 = *reinterpret_cast<const float4*>(g + I + j);
-    gvv[0] = a4.x; gvv[1] = a4.y; gvv[2] = a4.z; gvv[3] = a4.w;
-    ggg[0] = b4.x; ggg[1] = b4.y; ggg[2] = b4.z; ggg[3] = b4.w;
+    f32x8(g + j, gv);
+    f32x8(g + I + j, gg);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) igv[e] = 1.f / gv[e], igg[e] = 1.f / gg[e];
     if (bias) {
-      const float4 c4 = *reinterpret_cast<const float4*>(bias + j), d4 = *reinterpret_cast<const float4*>(bias + I + j);
-      bvv[0] = c4.x; bvv[1] = c4.y; bvv[2] = c4.z; bvv[3] = c4.w;
-      bgg[0] = d4.x; bgg[1] = d4.y; bgg[2] = d4.z; bgg[3] = d4.w;
+      f32x8(bias + j, bv);
+      f32x8(bias + I + j, bg);
     }
   }
-  float accv[4] = {0.f, 0.f, 0.f, 0.f}, accg[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int tb = t0; tb < t1; tb += 2) {
-    uint2 v2[2], g2[2], d2[2];
+  float accv[8], accg[8];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {                    // both rows' loads first
+  for (int e = 0; e < 8; ++e) accv[e] = accg[e] = 0.f;
+  for (int tb = t0; tb < t1; tb += kSwiRows) {
+    uint4 v4[kSwiRows], g4[kSwiRows], d4[kSwiRows];
+#pragma unroll
+    for (int u = 0; u < kSwiRows; ++u) {             // every row's loads first
       const int t = min(tb + u, t1 - 1);
       const __half* fr = f + (long)t * 2 * I;
-      v2[u] = *reinterpret_cast<const uint2*>(fr + j);
-      g2[u] = *reinterpret_cast<const uint2*>(fr + I + j);
-      d2[u] = *reinterpret_cast<const uint2*>(da + (long)t * I + j);
+      v4[u] = *reinterpret_cast<const uint4*>(fr + j);
+      g4[u] = *reinterpret_cast<const uint4*>(fr + I + j);
+      d4[u] = *reinterpret_cast<const uint4*>(da + (long)t * I + j);
     }
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
+    for (int u = 0; u < kSwiRows; ++u) {
       const int t = tb + u;
       if (t >= t1) break;
-      float vv[4], gg[4], dd[4];
-      f16x4(v2[u], vv);
-      f16x4(g2[u], gg);
-      f16x4(d2[u], dd);
-      float dv[4], dgl[4];
+      float vv[8], ga[8], dd[8], dv[8], dgl[8];
+      f16x8(v4[u], vv);
+      f16x8(g4[u], ga);
+      f16x8(d4[u], dd);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float sg = 1.f / (1.f + __expf(-gg[e]));
-        dv[e] = dd[e] * gg[e] * sg;
-        dgl[e] = dd[e] * vv[e] * sg * (1.f + gg[e] * (1.f - sg));
-      }
-      __half* zr = dz + (long)t * 2 * I;
-      dz_store4(zr + j, dv, gvv, dora);
-      dz_store4(zr + I + j, dgl, ggg, dora);
-      if (dora) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          accv[e] = fmaf(dv[e], (vv[e] - bvv[e]) / gvv[e], accv[e]);
-          accg[e] = fmaf(dgl[e], (gg[e] - bgg[e]) / ggg[e], accg[e]);
+      for (int e = 0; e < 8; ++e) {
+        const float sg = __fdividef(1.f, 1.f + __expf(-ga[e]));
+        dv[e] = dd[e] * ga[e] * sg;
+        dgl[e] = dd[e] * vv[e] * sg * (1.f + ga[e] * (1.f - sg));
+        if (dora) {
+          accv[e] = fmaf(dv[e], (vv[e] - bv[e]) * igv[e], accv[e]);
+          accg[e] = fmaf(dgl[e], (ga[e] - bg[e]) * igg[e], accg[e]);
+          dv[e] *= gv[e];
+          dgl[e] *= gg[e];
         }
       }
+      __half* zr = dz + (long)t * 2 * I;
+      *reinterpret_cast<uint4*>(zr + j) = f16x8_pack(dv);
+      *reinterpret_cast<uint4*>(zr + I + j) = f16x8_pack(dgl);
     }
   }
   if (dora) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 8; ++e) {
       atomicAdd(dg + j + e, accv[e]);
       atomicAdd(dg + I + j + e, accg[e]);
     }
@@ -577,11 +594,11 @@ int k_gate_bwd_dz(Ctx* c, const float* gx, const float* gate, long gstride, int 
 int k_swiglu_bwd_dz(Ctx* c, const __half* da, const __half* f, int T, int I, const float* bias,
                     const float* g,
                     __half* dz, float* dg, std::string& err) {
-  if (I % 4) { err = "swiglu: the hidden width must be a multiple of 4"; return 1; }
+  if (I % 8) { err = "swiglu: the hidden width must be a multiple of 8"; return 1; }
   if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 2 * I, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "swiglu_bwd_dz");
-  launch_pdl(c, swiglu_bwd_dz_kernel, dim3((unsigned)((I / 4 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)),
+  launch_pdl(c, swiglu_bwd_dz_kernel, dim3((unsigned)((I / 8 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)),
              128, 0, da, f, T, I, bias, g, dz, dg);
   return check_launch("swiglu_bwd_dz", err);
 }
@@ -620,6 +637,114 @@ int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, 
   ProfScope prof_(c, "dora_da_c3");
   launch_pdl(c, dora_da_c3_kernel, (unsigned)(((int64_t)rank * in + 255) / 256), 256, 0, c3, A, rank, in, dA);
   return check_launch("dora_da_c3", err);
+}
+
+
+// ---------------------------------------------------------------- rank-16 projections
+// u^T = f16(alpha (X Bm^T))^T for an adapter of rank <= 16: X [M][K] f16 (row stride ldx), Bm
+// [16][K] f16 (rows past the rank are zero), out [16][ldu] f16.  The forward's u = x A^T and the
+// backward's du = s dz B have this shape.  16 outputs per row make it a pure stream of X (2 bytes
+// per element against 32 FLOPs): the kernel is shaped for HBM, not for the tensor pipe (a
+// 128-row tcgen05 tile gives a 4352-row X only 34 CTAs, which cannot pull HBM's rate).
+// Block = 8 warps on 16 rows; each warp streams a contiguous eighth of the 32-wide k chunks,
+// keeping the X loads of the next 4 chunks in flight while it multiplies the current 4, with
+// warp-level m16n8k16 MMAs (two n-halves of the 16 outputs); the eight partial tiles are summed
+// in shared memory.  Within a chunk the k order is permuted so that a lane reads its X row slice
+// and its Bm slice as one 16-byte load each: lane (g, c) holds k 8c .. 8c + 7 of the chunk; the
+// first MMA takes k 8c .. 8c + 3 as its fragment pairs (2c, 2c + 8), the second k 8c + 4 .. 8c + 7.
+// X and Bm share the permutation, so the sum is unchanged.  Needs K % 32 == 0.
+constexpr int kR16Warps = 8, kR16Unroll = 4;
+
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__global__ void __launch_bounds__(32 * kR16Warps) r16_proj_kernel(const __half* __restrict__ x, long ldx, int M,
+                                                                   int K, const __half* __restrict__ bm, float alpha,
+                                                                   __half* __restrict__ ut, long ldu) {
+  pdl_prologue();
+  __shared__ float red[kR16Warps][16][17];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, c = lane & 3;
+  const int m0 = blockIdx.x * 16;
+  const long ra = min(m0 + g, M - 1), rb = min(m0 + g + 8, M - 1);   // clamped: stores are guarded
+  const __half* xa = x + ra * ldx + 8 * c;
+  const __half* xb = x + rb * ldx + 8 * c;
+  const __half* ba = bm + (long)g * K + 8 * c;
+  const __half* bb = bm + (long)(g + 8) * K + 8 * c;
+  float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+  // warp w streams the contiguous chunk range [c_lo, c_hi): at any moment the warps of a block
+  // read 8 different 512-byte row segments rather than one narrow column band of every row
+  const int nch = K / 32, per = (nch + kR16Warps - 1) / kR16Warps;
+  const int c_lo = warp * per, c_hi = min(nch, c_lo + per);
+  // two register groups of kR16Unroll chunks: the next group's loads are in flight while the
+  // current one is multiplied
+  uint4 a0[kR16Unroll], b0[kR16Unroll], a1[kR16Unroll], b1[kR16Unroll];
+  auto load = [&](uint4 (&va)[kR16Unroll], uint4 (&vb)[kR16Unroll], int ch0) {
+#pragma unroll
+    for (int u = 0; u < kR16Unroll; ++u) {
+      const int ch = min(ch0 + u, c_hi - 1);
+      va[u] = __ldcs(reinterpret_cast<const uint4*>(xa + 32 * ch));
+      vb[u] = __ldcs(reinterpret_cast<const uint4*>(xb + 32 * ch));
+    }
+  };
+  auto mul = [&](const uint4 (&va)[kR16Unroll], const uint4 (&vb)[kR16Unroll], int ch0) {
+#pragma unroll
+    for (int u = 0; u < kR16Unroll; ++u) {
+      const int ch = ch0 + u;
+      if (ch >= c_hi) break;
+      const uint4 wa = __ldg(reinterpret_cast<const uint4*>(ba + 32 * ch));   // Bm: L1 / L2 resident
+      const uint4 wb = __ldg(reinterpret_cast<const uint4*>(bb + 32 * ch));
+      mma_16816(d0, va[u].x, vb[u].x, va[u].y, vb[u].y, wa.x, wa.y);
+      mma_16816(d1, va[u].x, vb[u].x, va[u].y, vb[u].y, wb.x, wb.y);
+      mma_16816(d0, va[u].z, vb[u].z, va[u].w, vb[u].w, wa.z, wa.w);
+      mma_16816(d1, va[u].z, vb[u].z, va[u].w, vb[u].w, wb.z, wb.w);
+    }
+  };
+  if (c_lo < c_hi) load(a0, b0, c_lo);
+  for (int ch0 = c_lo; ch0 < c_hi; ch0 += 2 * kR16Unroll) {
+    if (ch0 + kR16Unroll < c_hi) load(a1, b1, ch0 + kR16Unroll);
+    mul(a0, b0, ch0);
+    if (ch0 + kR16Unroll >= c_hi) break;
+    if (ch0 + 2 * kR16Unroll < c_hi) load(a0, b0, ch0 + 2 * kR16Unroll);
+    mul(a1, b1, ch0 + kR16Unroll);
+  }
+  // accumulator fragment: rows g, g + 8; outputs 2c, 2c + 1 (d0) and 8 + 2c, 8 + 2c + 1 (d1)
+  red[warp][g][2 * c] = d0[0];
+  red[warp][g][2 * c + 1] = d0[1];
+  red[warp][g + 8][2 * c] = d0[2];
+  red[warp][g + 8][2 * c + 1] = d0[3];
+  red[warp][g][8 + 2 * c] = d1[0];
+  red[warp][g][8 + 2 * c + 1] = d1[1];
+  red[warp][g + 8][8 + 2 * c] = d1[2];
+  red[warp][g + 8][8 + 2 * c + 1] = d1[3];
+  __syncthreads();
+#pragma unroll
+  for (int i = threadIdx.x; i < 256; i += 32 * kR16Warps) {
+    const int r = i >> 4, row = i & 15;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kR16Warps; ++w) v += red[w][row][r];
+    if (m0 + row < M) ut[(long)r * ldu + m0 + row] = __float2half_rn(alpha * v);
+  }
+}
+
+int k_r16_proj(Ctx* c, const __half* x, long ldx, int64_t M, int64_t K, const __half* bm, float alpha, __half* ut,
+               long ldu, const char* name, std::string& err) {
+  if (M <= 0 || K <= 0 || K % 32 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(bm) & 15)) {
+    err = "rank-16 projection: K must be a positive multiple of 32 and the operands 16-byte aligned";
+    return 1;
+  }
+  if ((M + 15) / 16 > 0x7fffffffL) { err = "rank-16 projection: too many rows"; return 1; }
+  ProfScope prof_(c, name);
+  launch_pdl(c, r16_proj_kernel, dim3((unsigned)((M + 15) / 16)), 32 * kR16Warps, 0, x, ldx, (int)M, (int)K, bm, alpha,
+             ut, ldu);
+  return check_launch("r16_proj", err);
 }
 
 }  // namespace sa3k

@@ -50,6 +50,10 @@ int k_dora_bwd(Ctx* c, const float* pt, const float* B, int rank, int64_t out, c
                const float* nsq, const float* g, const float* dg, float s, float* dm, int dm_acc,
                float* dB, __half* cb, float* c3, std::string& err);
 int k_dora_da_c3(Ctx* c, const float* c3, const float* A, int rank, int64_t in, float* dA, std::string& err);
+// ut = f16(alpha X Bm^T)^T for a rank <= 16 adapter: X [M][K] f16 (row stride ldx), Bm [16][K] f16,
+// ut [16][ldu]; K % 32 == 0, 16-byte aligned operands (the forward's u = x A^T, the backward's du).
+int k_r16_proj(Ctx* c, const __half* x, long ldx, int64_t M, int64_t K, const __half* bm, float alpha, __half* ut,
+               long ldu, const char* name, std::string& err);
 
 // adamw.cu
 int k_sumsq(Ctx* c, const float* g, int64_t n, float inv, double* acc, std::string& err);
