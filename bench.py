@@ -423,6 +423,38 @@ def dit_attention_flops(cfg, B, T, C):
     return cfg["depth"] * (self_f * (1 + 2.5) + cross_f * (1 + 1.5))
 
 
+def dit_row_kernel_bytes(cfg, B, T, C):
+    """Algorithmic HBM bytes per step of the memory-bound kernel classes of the DiT step (what each
+    launch must read and write once: f32 = 4 B, f16 = 2 B per element; M = B (mem + T) token rows,
+    MC = B C context rows), for the achieved-bandwidth figures beside the kernel times."""
+    D, I, L = cfg["dim"], cfg["ff_inner"], cfg["depth"]
+    Q = (5 if cfg["differential"] else 3)
+    M, MC = B * (cfg["mem_tokens"] + T), B * C
+    blk = {
+        # x_in, y (f32) in; x_out (f32), h (f16) out
+        "residual_norm": 14.0 * M * D * 3,
+        # dh, x, gx in; gx out (f32); the feed-forward norm also writes gx as f16
+        "rmsnorm_mod_bwd": 16.0 * M * D * 3 + 2.0 * M * D,
+        # qkv f16 in / out; cross q f32 in, f16 out; cross kv (context rows) f32 in, f16 out
+        "head_prep_fwd": 4.0 * M * Q * D + 6.0 * M * D + 12.0 * MC * D,
+        # cross q gradient (f32) and its f32 projection output in, f16 dz out
+        "head_prep_bwd": 10.0 * M * D,
+        # attention gradients (f32) and qkv (f16) in, dz (f16) out
+        "qkv_bwd_dz": 4.0 * M * Q * D + 2.0 * M * Q * D + 2.0 * M * Q * D + (4.0 * M * D if Q == 5 else 0.0),
+        # gx, y (f32) in, dz (f16) out: feed-forward out and self-attention out
+        "gate_bwd_dz": 10.0 * M * D * 2,
+        "swiglu_fwd": 6.0 * M * I,
+        "swiglu_bwd_dz": 10.0 * M * I,
+        # u = x A^T of qkv, out, ff.proj (width D) and ff.out (width I): x (f16) streamed once
+        "lora.u": 2.0 * M * (3 * D + I),
+        # du = s dz B: dz (f16) of qkv, out, ff.proj, ff.out
+        "lora.du": 2.0 * M * (Q * D + D + 2 * I + D),
+        # dB = s dz^T u and dA = du^T x of all adapters: dz and x streamed once each
+        "lora.grads": 2.0 * M * (Q * D + D + 2 * I + D) + 2.0 * M * (3 * D + I),
+    }
+    return {k: v * L for k, v in blk.items()}
+
+
 def build_dit(ctx, cfg, seed, adapter_type="dora-rows"):
     """A seeded synthetic checkpoint uploaded as GGUF Q8_0 rows (weights made and encoded on the GPU)."""
     import torch
@@ -751,6 +783,14 @@ def main_dit(args):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = dit_cpu_baseline(cfg)
     step_flops = gflops + dit_attention_flops(cfg, B, T, C)
+    # achieved bandwidth of the memory-bound classes: algorithmic bytes / their summed CUDA-event time
+    membound = {"peak_gbs": peak_hbm, "peak_kind": f"{peak_kind} HBM copy"}
+    for name, nbytes in dit_row_kernel_bytes(cfg, B, T, C).items():
+        if name in prof and prof[name][1] > 0:
+            ms_k = prof[name][1] / kprof
+            gbs = nbytes / (ms_k / 1000.0) / 1e9
+            membound[name] = {"ms_per_step": round(ms_k, 4), "gb_per_step": round(nbytes / 1e9, 3),
+                              "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_hbm, 3)}
     if rank == 0:
         ms_step = total_ms / args.steps
         line = {
@@ -782,6 +822,7 @@ def main_dit(args):
             "graph": "fwd+bwd replayed from a CUDA graph; gradient all-reduce (NCCL, N > 1) + AdamW launched "
                      "eagerly per step through sa3k_dit_dp_apply_adamw / sa3k_dit_apply_adamw",
             "kernels": {k: {"launches": v[0], "ms_per_step": round(v[1] / kprof, 4)} for k, v in sorted(prof.items())},
+            "memory_bound_kernels": membound,
         }
         print(json.dumps(line), flush=True)
     ctx.sync()

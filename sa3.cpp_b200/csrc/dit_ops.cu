@@ -39,6 +39,7 @@ struct HeadSlices {
 };
 constexpr int kHpRows = 16;
 constexpr int kQkvRows = 32;   // qkv_bwd_dz: more rows per block, fewer dg atomics
+constexpr int kQkvSets = 4;    // qkv_bwd_dz: row sets whose loads are in flight together
 
 __device__ __forceinline__ float sum8(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 1);
@@ -391,63 +392,75 @@ __global__ void __launch_bounds__(256, 2) qkv_bwd_dz_kernel(const float* __restr
 #pragma unroll
   for (int k = 0; k < 8; ++k) acc[k] = 0.f;
   const int tb0 = blockIdx.y * kQkvRows;
-  int pos = (tb0 + q) % tps;
-  // the next row's loads are issued before this row is processed (the dz stores in between may
+  float igd[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) igd[k] = g ? 1.f / gd[k] : 1.f;
+  // kQkvSets row sets in flight per thread: their raw loads (f32 gradient as two float4, f16 qkv
+  // as one uint4) are all issued before any of them is processed (the dz stores in between may
   // alias the inputs for the compiler)
-  float gvn[8], yvn[8], rn = 0.f;
-  auto fetch = [&](int it) {
-    const int t = tb0 + 4 * it + q;
-    rn = 0.f;
-    if (it < kQkvRows / 4 && t < T) {
-      ld8(dq3 + (long)t * ncols + col, gvn);
-      if (norm || g) ld8(qkv + (long)t * ncols + col, yvn);
-      if (norm) rn = rs[(long)t * H + h];
-    } else {
+  for (int it0 = 0; it0 < kQkvRows / 4 && tb0 + 4 * it0 < T; it0 += kQkvSets) {
+    float4 ga[kQkvSets][2];
+    uint4 ya[kQkvSets];
+    float ra[kQkvSets];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) gvn[k] = yvn[k] = 0.f;
-    }
-  };
-  fetch(0);
-#pragma unroll 1
-  for (int it = 0; it < kQkvRows / 4 && tb0 + 4 * it < T; ++it) {
-  {
-    const int t = tb0 + 4 * it + q;
-    const bool valid = t < T;
-    float gv[8], yv[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) gv[k] = gvn[k], yv[k] = yvn[k];
-    const float r = rn;
-    fetch(it + 1);
-    if (valid && sub_dv2) {
-      float w[8];
-      ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] -= w[k];
-    }
-    if (sgn < 0.f) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] = -gv[k];
-    }
-    if (norm) {
-      if (rot == 32 || rot == 64) rope8(gv, j, pos, rot, tab, true);
-      float dot = 0.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) dot = fmaf(gv[k] * gm[k], yv[k] * r, dot);
-      const float mean = sum8(dot) / 64.f;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] = r * (gv[k] * gm[k] - yv[k] * r * mean);
-    }
-    if (g) {
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        acc[k] = fmaf(gv[k], yv[k] / gd[k], acc[k]);
-        gv[k] *= gd[k];
+    for (int u = 0; u < kQkvSets; ++u) {
+      const int t = tb0 + 4 * (it0 + u) + q;
+      ra[u] = 0.f;
+      if (it0 + u < kQkvRows / 4 && t < T) {
+        const float4* gp = reinterpret_cast<const float4*>(dq3 + (long)t * ncols + col);
+        ga[u][0] = gp[0];
+        ga[u][1] = gp[1];
+        ya[u] = (norm || g) ? *reinterpret_cast<const uint4*>(qkv + (long)t * ncols + col) : make_uint4(0u, 0u, 0u, 0u);
+        if (norm) ra[u] = rs[(long)t * H + h];
+      } else {
+        ga[u][0] = ga[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        ya[u] = make_uint4(0u, 0u, 0u, 0u);
       }
     }
-    if (valid) st8_f16(dz + (long)t * ncols + col, gv);
-    pos += 4;
-    while (pos >= tps) pos -= tps;
-  }
+#pragma unroll
+    for (int u = 0; u < kQkvSets; ++u) {
+      const int t = tb0 + 4 * (it0 + u) + q;
+      const bool valid = it0 + u < kQkvRows / 4 && t < T;
+      float gv[8] = {ga[u][0].x, ga[u][0].y, ga[u][0].z, ga[u][0].w, ga[u][1].x, ga[u][1].y, ga[u][1].z, ga[u][1].w};
+      float yv[8];
+      {
+        const uint32_t yw[4] = {ya[u].x, ya[u].y, ya[u].z, ya[u].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&yw[k]));
+          yv[2 * k] = f.x;
+          yv[2 * k + 1] = f.y;
+        }
+      }
+      const float r = ra[u];
+      if (valid && sub_dv2) {
+        float w[8];
+        ld8(dv2 + (long)t * D + h * 64 + 8 * j, w);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] -= w[k];
+      }
+      if (sgn < 0.f) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] = -gv[k];
+      }
+      if (norm) {
+        if (rot == 32 || rot == 64) rope8(gv, j, (valid ? t : 0) % tps, rot, tab, true);
+        float dot = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dot = fmaf(gv[k] * gm[k], yv[k] * r, dot);
+        const float mean = sum8(dot) / 64.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) gv[k] = r * (gv[k] * gm[k] - yv[k] * r * mean);
+      }
+      if (g) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          acc[k] = fmaf(gv[k], yv[k] * igd[k], acc[k]);
+          gv[k] *= gd[k];
+        }
+      }
+      if (valid) st8_f16(dz + (long)t * ncols + col, gv);
+    }
   }
   if (g) {
 #pragma unroll
