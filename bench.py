@@ -997,16 +997,19 @@ def attn_dit_case(a):
     ctx = sa3k.Context(0)
     g = torch.Generator(device="cuda").manual_seed(0)
     B, H, S = a.b, a.h, a.s
-    bf = lambda: torch.randn(B, S, H * 64, generator=g, device="cuda").to(torch.float16)
-    q, k, v, dO = bf(), bf(), bf(), bf()
+    Sk = a.sk if a.sk > 0 else S        # --sk 128: the cross-attention shape (context keys)
+    bf = lambda n: torch.randn(B, n, H * 64, generator=g, device="cuda").to(torch.float16)
+    q, dO = bf(S), bf(S)
+    k, v = bf(Sk), bf(Sk)
     o = torch.empty_like(q)
-    dq, dk, dv = (torch.empty(B, S, H * 64, device="cuda") for _ in range(3))
+    dq = torch.empty(B, S, H * 64, device="cuda")
+    dk, dv = (torch.empty(B, Sk, H * 64, device="cuda") for _ in range(2))
     lse = torch.empty(B * H * S, device="cuda")
-    st = (S * H * 64, 64, H * 64)
+    st, sk = (S * H * 64, 64, H * 64), (Sk * H * 64, 64, H * 64)
     T4 = sa3k.t4
-    fwd = lambda: ctx.attention_fwd(B, H, S, S, 0.125, a.window, T4(q, *st), T4(k, *st), T4(v, *st), T4(o, *st), lse)
-    bwd = lambda: ctx.attention_bwd(B, H, S, S, 0.125, a.window, T4(q, *st), T4(k, *st), T4(v, *st), T4(o, *st),
-                                    T4(dO, *st), lse, T4(dq, *st), T4(dk, *st), T4(dv, *st))
+    fwd = lambda: ctx.attention_fwd(B, H, S, Sk, 0.125, a.window, T4(q, *st), T4(k, *sk), T4(v, *sk), T4(o, *st), lse)
+    bwd = lambda: ctx.attention_bwd(B, H, S, Sk, 0.125, a.window, T4(q, *st), T4(k, *sk), T4(v, *sk), T4(o, *st),
+                                    T4(dO, *st), lse, T4(dq, *st), T4(dk, *sk), T4(dv, *sk))
     for _ in range(a.warmup):
         fwd()
         bwd()
@@ -1020,7 +1023,7 @@ def attn_dit_case(a):
     ctx.sync()
     if a.time:
         for name, (n, ms) in sorted(ctx.profile_read().items()):
-            print(f"attention B{B} H{H} S{S} window {a.window}: {name} {ms / n * 1e3:.1f} us/launch")
+            print(f"attention B{B} H{H} S{S} Sk{Sk} window {a.window}: {name} {ms / n * 1e3:.1f} us/launch")
     ctx.close()
 
 
@@ -1116,6 +1119,7 @@ def kernel_case(workload, argv):
         ap.add_argument("--h", type=int, default=24)
         ap.add_argument("--s", type=int, default=1088)
         ap.add_argument("--window", type=int, default=-1)
+        ap.add_argument("--sk", type=int, default=0)
         ap.add_argument("--fwd-only", action="store_true")
         return attn_dit_case(ap.parse_args(argv))
     ap.add_argument("--type", default="bora")

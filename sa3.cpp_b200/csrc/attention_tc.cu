@@ -1022,6 +1022,471 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   }
 }
 
+// ============================================================================== short key range
+// Attention whose keys fit one 128-wide tile (1 <= Sk <= 128, no band): the cross-attention to the
+// 128 conditioning tokens.  With one or two 64-key tiles per 128 queries, the general kernels spend
+// each CTA on load / MMA / softmax / epilogue latencies in series.  These kernels are persistent
+// over 128-query items (CTA c takes a contiguous range of them), load an item's Q (dO, O) and the
+// head's whole K / V in one TMA transaction into one of two buffers (K / V only when the buffer's
+// previous item had another head), and keep two items in flight:
+// softmax warpgroup g takes the CTA's items i with i % 2 == g, on its own TMEM buffer, while the
+// MMA warp already issues the next item's score MMAs.  Keys at or past Sk (TMA zero fill) are
+// masked to -inf.
+constexpr int SF_BUF = 3 * 16384;                 // forward: Q | K | V of one item
+constexpr int SF_STG = 8 * 4096;                  // forward: 32 rows x 128 B of O per softmax warp
+constexpr int SF_SMEM = 2 * SF_BUF + SF_STG + 256;
+constexpr int SQ_BUF = 5 * 16384;                 // dq pass: Q | dO | O | K | V of one item
+constexpr int SQ_STG = 8 * 8192;                  // dq pass: 32 rows x 256 B of dQ per softmax warp
+constexpr int SQ_SMEM = 2 * SQ_BUF + SQ_STG + 256;
+
+// CTA c's items: a contiguous range of the (b, h, 128-query tile) order, so that consecutive items
+// of a CTA mostly share their head and a buffer's K / V can stay in place
+__device__ __forceinline__ void short_range(int nitems, int& first, int& n) {
+  const int G = (int)gridDim.x, c = (int)blockIdx.x, per = nitems / G, rem = nitems % G;
+  first = c * per + min(c, rem);
+  n = per + (c < rem ? 1 : 0);
+}
+
+// Forward.  TMEM buffer g at 192 g: S [0, 128) (P overwrites [0, 64) as packed f16), O [128, 192).
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    attn_short_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sstg = smem + 2 * SF_BUF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sstg + SF_STG);
+  uint64_t* in_full = bars;            // [2] TMA -> MMA
+  uint64_t* in_empty = in_full + 2;    // [2] P V done -> TMA
+  uint64_t* s_full = in_empty + 2;     // [2] S MMAs done -> softmax
+  uint64_t* p_full = s_full + 2;       // [2] P in TMEM -> MMA (one arrival per softmax warp)
+  uint64_t* o_full = p_full + 2;       // [2] P V done -> epilogue
+  uint64_t* o_empty = o_full + 2;      // [2] epilogue read O -> the buffer's next S MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qtiles = (a.Sq + 127) / 128, nitems = a.B * a.H * qtiles;
+  int first, n;
+  short_range(nitems, first, n);
+  auto item_of = [&](int i, int& b, int& h, int& bh, int& q0) {
+    const int item = first + i;
+    bh = item / qtiles;
+    q0 = (item % qtiles) * 128;
+    b = bh / a.H;
+    h = bh % a.H;
+  };
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&in_full[i], 1);
+      mbar_init(&in_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  pdl_wait();
+  const Waiter wait{abort_flag, a.err};
+  const WaiterW<> waitw{abort_flag, a.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        int b, h, bh, q0;
+        item_of(i, b, h, bh, q0);
+        const int bf = i & 1;
+        if (i >= 2 && !wait(&in_empty[bf], (uint32_t)(((i >> 1) - 1) & 1), kErrTimeoutEmpty)) break;
+        uint8_t* buf = smem + bf * SF_BUF;
+        int pb, ph_, pbh = -1, pq;
+        if (i >= 2) item_of(i - 2, pb, ph_, pbh, pq);
+        const bool kv = pbh != bh;     // the buffer holds another head's K / V
+        mbar_arrive_expect_tx(&in_full[bf], (uint32_t)(kv ? SF_BUF : 16384));
+        load_rows(buf, &tm_q, &in_full[bf], a.q_tm, b, h, q0);
+        if (kv) {
+          load_rows(buf + 16384, &tm_k, &in_full[bf], a.k_tm, b, h, 0);
+          load_rows(buf + 32768, &tm_v, &in_full[bf], a.v_tm, b, h, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);   // S[128 q][128 k] = Q K^T
+    const uint32_t id_o = make_idesc_f16(128, 64, 0, 1);    // O[128 q][64 d] = P V (V MN-major)
+    auto issue_s = [&](int i) -> bool {
+      const int bf = i & 1;
+      if (!waitw(&in_full[bf], (uint32_t)((i >> 1) & 1), kErrTimeoutFull)) return false;
+      if (i >= 2 && !waitw(&o_empty[bf], (uint32_t)(((i >> 1) - 1) & 1), kErrTimeoutOther)) return false;
+      tc_fence_after();
+      const uint32_t ba = smem_u32(smem + bf * SF_BUF);
+      const uint64_t qd = kdesc0(ba), kd = kdesc0(ba + 16384);
+      const uint32_t tS = tbase + 192 * bf;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
+      umma_commit_w(&s_full[bf]);
+      return true;
+    };
+    bool ok = n == 0 || issue_s(0);
+    for (int i = 0; i < n && ok; ++i) {
+      const int bf = i & 1;
+      if (i + 1 < n && !issue_s(i + 1)) { ok = false; break; }
+      if (!waitw(&p_full[bf], (uint32_t)((i >> 1) & 1), kErrTimeoutReady)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t vd = mndesc0(smem_u32(smem + bf * SF_BUF + 32768));
+      const uint32_t tS = tbase + 192 * bf, tO = tS + 128;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)   // 128 keys = 8 k-steps; P at S columns [0, 64)
+        umma_ts_w(tO, tS + kk * 8, mnstep(vd, kk), id_o, kk > 0 ? 1u : 0u);
+      umma_commit_w(&o_full[bf]);
+      umma_commit_w(&in_empty[bf]);
+    }
+  } else if (warp < 10) {
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = 32 * quarter + lane;
+    const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+    const uint32_t tS = tbase + 192 * g, tO = tS + 128;
+    bool ok = true;
+    for (int i = g; i < n && ok; i += 2) {
+      int b, h, bh, q0;
+      item_of(i, b, h, bh, q0);
+      const int qi = q0 + row;
+      const uint32_t ph = (uint32_t)((i >> 1) & 1);
+      if (!waitw(&s_full[g], ph, kErrTimeoutAccum)) { ok = false; break; }
+      tc_fence_after();
+      // pass 1: the row max over the visible keys
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_off + 32 * c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          if (32 * c + e < a.Sk) mx = fmaxf(mx, __uint_as_float(v[e]));
+      }
+      const float mb = mx == -INFINITY ? 0.f : mx * a.sl2;   // (scale > 0 keeps the order)
+      // pass 2: P = 2^(s scale log2 e - m) as packed f16; chunk c's 32 keys go to columns
+      // [16 c, 16 c + 16), which the later chunks no longer read
+      const uint64_t sc2 = f2(a.sl2, a.sl2), nb2 = f2(-mb, -mb);
+      uint64_t lsum[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_off + 32 * c, v);
+        tmem_ld_wait();
+        if (32 * c + 32 > a.Sk) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            if (32 * c + e >= a.Sk) v[e] = __float_as_uint(-INFINITY);
+        }
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float x0, x1, p0, p1;
+          f2split(ffma2(f2(__uint_as_float(v[2 * e]), __uint_as_float(v[2 * e + 1])), sc2, nb2), x0, x1);
+          if (kPolyPair[e & 7]) {
+            ex2_poly2(x0, x1, p0, p1);
+            if (32 * c + 2 * e >= a.Sk) p0 = 0.f;       // (the polynomial clamps -inf to 2^-125)
+            if (32 * c + 2 * e + 1 >= a.Sk) p1 = 0.f;
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          lsum[e & 1] = fadd2(lsum[e & 1], f2(p0, p1));
+          pk[e] = pack_f16x2(p0, p1);
+        }
+        tmem_st16(tS + lane_off + 16 * c, pk);
+      }
+      float l;
+      {
+        float l0, l1, l2, l3;
+        f2split(lsum[0], l0, l1);
+        f2split(lsum[1], l2, l3);
+        l = (l0 + l1) + (l2 + l3);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[g]);
+      // epilogue: O / l to the f16 output, the row's log2-sum-exp
+      if (!waitw(&o_full[g], ph, kErrTimeoutAccum)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t o[64];
+      tmem_ld32(tO + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      tmem_ld32(tO + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_empty[g]);
+      // O / l through this warp's staging rows (16-byte chunk c of row r at c ^ (r & 7)), then
+      // stored four rows (4 x 128 contiguous bytes) per warp instruction
+      {
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint8_t* stg = sstg + (warp - 2) * 4096;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 w4;
+          w4.x = pack_f16x2(__uint_as_float(o[8 * c]) * inv, __uint_as_float(o[8 * c + 1]) * inv);
+          w4.y = pack_f16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv);
+          w4.z = pack_f16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv);
+          w4.w = pack_f16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv);
+          *reinterpret_cast<uint4*>(stg + lane * 128 + ((c ^ (lane & 7)) << 4)) = w4;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int r = 4 * it + (lane >> 3), c = lane & 7, qr = q0 + 32 * quarter + r;
+          const uint4 w4 = *reinterpret_cast<const uint4*>(stg + r * 128 + ((c ^ (r & 7)) << 4));
+          if (qr < a.Sq) reinterpret_cast<uint4*>(a.o + b * a.o_sb + h * a.o_sh + (long)qr * a.o_ld)[c] = w4;
+        }
+        __syncwarp();
+        if (qi < a.Sq && a.lse) a.lse[(long)bh * a.Sq + qi] = mb + log2f(fmaxf(l, 1e-30f));
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// dQ pass (and D = rowsum(dO o O) for the dk / dv pass).  TMEM buffer g at 256 g: S [0, 128) (dS
+// overwrites [0, 64) as packed f16), dP [128, 256) (dQ accumulates into [128, 192) once every dP
+// value has been read).
+__global__ void __launch_bounds__(kThreadsTC, 1)
+    attn_short_dq_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_do,
+                         const __grid_constant__ CUtensorMap tm_o, const __grid_constant__ CUtensorMap tm_k,
+                         const __grid_constant__ CUtensorMap tm_v, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  pdl_trigger();
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sstg = smem + 2 * SQ_BUF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sstg + SQ_STG);
+  uint64_t* in_full = bars;            // [2] TMA -> MMA and softmax (D)
+  uint64_t* in_empty = in_full + 2;    // [2] dQ MMAs done -> TMA
+  uint64_t* sp_full = in_empty + 2;    // [2] S and dP MMAs done -> softmax
+  uint64_t* ds_full = sp_full + 2;     // [2] dS in TMEM -> MMA (one arrival per softmax warp)
+  uint64_t* dq_full = ds_full + 2;     // [2] dQ MMAs done -> epilogue
+  uint64_t* dq_empty = dq_full + 2;    // [2] epilogue read dQ -> the buffer's next MMAs
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qtiles = (a.Sq + 127) / 128, nitems = a.B * a.H * qtiles;
+  int first, n;
+  short_range(nitems, first, n);
+  auto item_of = [&](int i, int& b, int& h, int& bh, int& q0) {
+    const int item = first + i;
+    bh = item / qtiles;
+    q0 = (item % qtiles) * 128;
+    b = bh / a.H;
+    h = bh % a.H;
+  };
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&in_full[i], 1);
+      mbar_init(&in_empty[i], 1);
+      mbar_init(&sp_full[i], 1);
+      mbar_init(&ds_full[i], 4);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_do);
+    tma_prefetch_desc(&tm_o);
+    tma_prefetch_desc(&tm_k);
+    tma_prefetch_desc(&tm_v);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  pdl_wait();
+  const Waiter wait{abort_flag, a.err};
+  const WaiterW<> waitw{abort_flag, a.err};
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < n; ++i) {
+        int b, h, bh, q0;
+        item_of(i, b, h, bh, q0);
+        const int bf = i & 1;
+        if (i >= 2 && !wait(&in_empty[bf], (uint32_t)(((i >> 1) - 1) & 1), kErrTimeoutEmpty)) break;
+        uint8_t* buf = smem + bf * SQ_BUF;
+        int pb, ph_, pbh = -1, pq;
+        if (i >= 2) item_of(i - 2, pb, ph_, pbh, pq);
+        const bool kv = pbh != bh;     // the buffer holds another head's K / V
+        mbar_arrive_expect_tx(&in_full[bf], (uint32_t)(kv ? SQ_BUF : 49152));
+        load_rows(buf, &tm_q, &in_full[bf], a.q_tm, b, h, q0);
+        load_rows(buf + 16384, &tm_do, &in_full[bf], a.do_tm, b, h, q0);
+        load_rows(buf + 32768, &tm_o, &in_full[bf], a.o_tm, b, h, q0);
+        if (kv) {
+          load_rows(buf + 49152, &tm_k, &in_full[bf], a.k_tm, b, h, 0);
+          load_rows(buf + 65536, &tm_v, &in_full[bf], a.v_tm, b, h, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t id_s = make_idesc_f16(128, 128, 0, 0);    // S = Q K^T, dP = dO V^T  [128 q][128 k]
+    const uint32_t id_dq = make_idesc_f16(128, 64, 0, 1);    // dQ[128 q][64 d] = dS K (K MN-major)
+    auto issue_sp = [&](int i) -> bool {
+      const int bf = i & 1;
+      if (!waitw(&in_full[bf], (uint32_t)((i >> 1) & 1), kErrTimeoutFull)) return false;
+      if (i >= 2 && !waitw(&dq_empty[bf], (uint32_t)(((i >> 1) - 1) & 1), kErrTimeoutOther)) return false;
+      tc_fence_after();
+      const uint32_t ba = smem_u32(smem + bf * SQ_BUF);
+      const uint64_t qd = kdesc0(ba), dd = kdesc0(ba + 16384), kd = kdesc0(ba + 49152), vd = kdesc0(ba + 65536);
+      const uint32_t tS = tbase + 256 * bf;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS, kstep(qd, kk), kstep(kd, kk), id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) umma_f16_w(tS + 128, kstep(dd, kk), kstep(vd, kk), id_s, kk > 0 ? 1u : 0u);
+      umma_commit_w(&sp_full[bf]);
+      return true;
+    };
+    bool ok = n == 0 || issue_sp(0);
+    for (int i = 0; i < n && ok; ++i) {
+      const int bf = i & 1;
+      if (i + 1 < n && !issue_sp(i + 1)) { ok = false; break; }
+      if (!waitw(&ds_full[bf], (uint32_t)((i >> 1) & 1), kErrTimeoutReady)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t kmn = mndesc0(smem_u32(smem + bf * SQ_BUF + 49152));
+      const uint32_t tS = tbase + 256 * bf, tQ = tS + 128;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)   // 128 keys = 8 k-steps; dS at S columns [0, 64)
+        umma_ts_w(tQ, tS + kk * 8, mnstep(kmn, kk), id_dq, kk > 0 ? 1u : 0u);
+      umma_commit_w(&dq_full[bf]);
+      umma_commit_w(&in_empty[bf]);
+    }
+  } else if (warp < 10) {
+    const int g = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = 32 * quarter + lane;
+    const uint32_t lane_off = (uint32_t)(32 * quarter) << 16;
+    const uint32_t tS = tbase + 256 * g, tP = tS + 128;
+    bool ok = true;
+    for (int i = g; i < n && ok; i += 2) {
+      int b, h, bh, q0;
+      item_of(i, b, h, bh, q0);
+      const int qi = q0 + row;
+      const bool qok = qi < a.Sq;
+      const uint32_t ph = (uint32_t)((i >> 1) & 1);
+      const float lse = qok ? a.lse_in[(long)bh * a.Sq + qi] : INFINITY;
+      if (!waitw(&in_full[g], ph, kErrTimeoutFull)) { ok = false; break; }
+      // D = rowsum(dO o O) from the swizzled dO and O tiles in shared memory
+      float Dq = 0.f;
+      {
+        const uint8_t* sdO = smem + g * SQ_BUF + 16384;
+        const uint8_t* sO = sdO + 16384;
+#pragma unroll
+        for (int cc = 0; cc < 8; ++cc) {
+          const int off = row * 128 + ((cc ^ (row & 7)) << 4);
+          const uint4 ov = *reinterpret_cast<const uint4*>(sO + off);
+          const uint4 dv = *reinterpret_cast<const uint4*>(sdO + off);
+          const __half2* o2 = reinterpret_cast<const __half2*>(&ov);
+          const __half2* d2 = reinterpret_cast<const __half2*>(&dv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 of = __half22float2(o2[e]), df = __half22float2(d2[e]);
+            Dq = fmaf(of.x, df.x, Dq);
+            Dq = fmaf(of.y, df.y, Dq);
+          }
+        }
+      }
+      if (!qok) Dq = 0.f;
+      if (qok) a.Dsum[(long)bh * a.Sq + qi] = Dq;
+      if (!waitw(&sp_full[g], ph, kErrTimeoutAccum)) { ok = false; break; }
+      tc_fence_after();
+      const uint64_t sc2 = f2(a.sl2, a.sl2), nl2 = f2(-lse, -lse), nd2 = f2(-Dq, -Dq);
+      // chunk c's 32 keys: S / dP in, dS (packed f16) out to columns [16 c, 16 c + 16)
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], pv[32];
+        tmem_ld32(tS + lane_off + 32 * c, sv);
+        tmem_ld32(tP + lane_off + 32 * c, pv);
+        tmem_ld_wait();
+        uint32_t pk[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float x0, x1, p0, p1, d0, d1;
+          f2split(ffma2(f2(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sc2, nl2), x0, x1);
+          if (kPolyPair[e & 7]) {
+            ex2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2(x0);
+            p1 = ex2(x1);
+          }
+          if (32 * c + 2 * e >= a.Sk) p0 = 0.f;        // keys past Sk (zero-filled rows)
+          if (32 * c + 2 * e + 1 >= a.Sk) p1 = 0.f;
+          f2split(fmul2(f2(p0, p1), fadd2(f2(__uint_as_float(pv[2 * e]), __uint_as_float(pv[2 * e + 1])), nd2)), d0,
+                  d1);
+          pk[e] = pack_f16x2(d0, d1);
+        }
+        tmem_st16(tS + lane_off + 16 * c, pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ds_full[g]);
+      // epilogue: scale dQ to the f32 output
+      if (!waitw(&dq_full[g], ph, kErrTimeoutAccum)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t o[64];
+      tmem_ld32(tP + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&o[0]));
+      tmem_ld32(tP + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&o[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dq_empty[g]);
+      // dQ through this warp's staging rows (16-byte chunk c of row r at c ^ (r & 15)), then
+      // stored two rows (2 x 256 contiguous bytes) per warp instruction
+      {
+        uint8_t* stg = sstg + (warp - 2) * 8192;
+#pragma unroll
+        for (int c = 0; c < 16; ++c)
+          *reinterpret_cast<float4*>(stg + lane * 256 + ((c ^ (lane & 15)) << 4)) =
+              make_float4(__uint_as_float(o[4 * c]) * a.scale, __uint_as_float(o[4 * c + 1]) * a.scale,
+                          __uint_as_float(o[4 * c + 2]) * a.scale, __uint_as_float(o[4 * c + 3]) * a.scale);
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 16; ++it) {
+          const int r = 2 * it + (lane >> 4), c = lane & 15, qr = q0 + 32 * quarter + r;
+          const float4 v4 = *reinterpret_cast<const float4*>(stg + r * 256 + ((c ^ (r & 15)) << 4));
+          if (qr < a.Sq) reinterpret_cast<float4*>(a.dq + b * a.dq_sb + h * a.dq_sh + (long)qr * a.dq_ld)[c] = v4;
+        }
+        __syncwarp();
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 // ------------------------------------------------------------------------------ host side
 // 4-D tensor map over a strided (b, h, s, d) tensor with 64 values per row (d): the smaller of
 // the head / row strides goes second so the strides grow; the box is `rows` rows x `box_d`
@@ -1082,8 +1547,13 @@ int set_tc_attrs(int device, std::string& err) {
   const char* what = "attention tc smem attributes";
   return smem_attr(reinterpret_cast<const void*>(attn_tc_fwd_kernel), smem_req(F_SMEM), device, what, err) ||
          smem_attr(reinterpret_cast<const void*>(attn_tc_dq_kernel), smem_req(Q_SMEM), device, what, err) ||
-         smem_attr(reinterpret_cast<const void*>(attn_tc_dkdv_kernel), smem_req(KV_SMEM), device, what, err);
+         smem_attr(reinterpret_cast<const void*>(attn_tc_dkdv_kernel), smem_req(KV_SMEM), device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_short_fwd_kernel), smem_req(SF_SMEM), device, what, err) ||
+         smem_attr(reinterpret_cast<const void*>(attn_short_dq_kernel), smem_req(SQ_SMEM), device, what, err);
 }
+
+// the keys fit one 128-wide tile and there is no band: the short-range kernels
+bool short_keys(const AttnArgs& p) { return p.Sk >= 1 && p.Sk <= 128 && p.window < 0; }
 
 }  // namespace
 
@@ -1104,11 +1574,18 @@ int attn_tc_forward(Ctx* c, const AttnArgs& p, std::string& err) {
   TcArgs a = tc_args(p);
   a.err = c->d_err;
   CUtensorMap mq, mk, mv;
+  const int kv_rows = short_keys(p) ? 128 : 64;
   if (make_map4(&mq, p.q, p.q_sb, p.q_sh, p.q_ld, p.B, p.H, p.Sq, 128, a.q_tm, err) ||
-      make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, 64, a.k_tm, err) ||
-      make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 64, a.v_tm, err))
+      make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, kv_rows, a.k_tm, err) ||
+      make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, kv_rows, a.v_tm, err))
     return 1;
   ProfScope prof_(c, "attn.fwd");
+  if (short_keys(p)) {   // persistent over 128-query items
+    const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);
+    const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
+    launch_pdl(c, attn_short_fwd_kernel, grid, kThreadsTC, smem_req(SF_SMEM), mq, mk, mv, a);
+    return check_launch("attn short fwd", err);
+  }
   dim3 grid((unsigned)((p.Sq + 255) / 256), (unsigned)(p.B * p.H));
   launch_pdl(c, attn_tc_fwd_kernel, grid, kThreadsTC, smem_req(F_SMEM), mq, mk, mv, a);
   return check_launch("attn tc fwd", err);
@@ -1120,19 +1597,33 @@ int attn_tc_grads(Ctx* c, const AttnArgs& p, bool want_dkdv, std::string& err) {
   a.err = c->d_err;
   {
     CUtensorMap mq, mdo, mk, mv, mo, mdq;
-    if (make_map4(&mq, p.q, p.q_sb, p.q_sh, p.q_ld, p.B, p.H, p.Sq, 128, a.q_tm, err) ||
-        make_map4(&mdo, p.dO, p.dO_sb, p.dO_sh, p.dO_ld, p.B, p.H, p.Sq, 128, a.do_tm, err) ||
-        make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, 64, a.k_tm, err) ||
-        make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 64, a.v_tm, err) ||
-        make_map4(&mo, p.o, p.o_sb, p.o_sh, p.o_ld, p.B, p.H, p.Sq, 128, a.o_tm, err) ||
-        make_map4t(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.dq, p.dq_sb, p.dq_sh, p.dq_ld, p.B, p.H, p.Sq, 32, 32,
-                   a.dq_tm, err))
-      return 1;
-    ProfScope prof_(c, "attn.bwd_dq");
-    const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);   // persistent: one CTA per SM at most
-    const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
-    launch_pdl(c, attn_tc_dq_kernel, grid, kThreadsTC, smem_req(Q_SMEM), mq, mdo, mk, mv, mo, mdq, a);
-    if (check_launch("attn tc dq", err)) return 1;
+    if (short_keys(p)) {
+      if (make_map4(&mq, p.q, p.q_sb, p.q_sh, p.q_ld, p.B, p.H, p.Sq, 128, a.q_tm, err) ||
+          make_map4(&mdo, p.dO, p.dO_sb, p.dO_sh, p.dO_ld, p.B, p.H, p.Sq, 128, a.do_tm, err) ||
+          make_map4(&mo, p.o, p.o_sb, p.o_sh, p.o_ld, p.B, p.H, p.Sq, 128, a.o_tm, err) ||
+          make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, 128, a.k_tm, err) ||
+          make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 128, a.v_tm, err))
+        return 1;
+      ProfScope prof_(c, "attn.bwd_dq");
+      const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);
+      const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
+      launch_pdl(c, attn_short_dq_kernel, grid, kThreadsTC, smem_req(SQ_SMEM), mq, mdo, mo, mk, mv, a);
+      if (check_launch("attn short dq", err)) return 1;
+    } else {
+      if (make_map4(&mq, p.q, p.q_sb, p.q_sh, p.q_ld, p.B, p.H, p.Sq, 128, a.q_tm, err) ||
+          make_map4(&mdo, p.dO, p.dO_sb, p.dO_sh, p.dO_ld, p.B, p.H, p.Sq, 128, a.do_tm, err) ||
+          make_map4(&mk, p.k, p.k_sb, p.k_sh, p.k_ld, p.B, p.H, p.Sk, 64, a.k_tm, err) ||
+          make_map4(&mv, p.v, p.v_sb, p.v_sh, p.v_ld, p.B, p.H, p.Sk, 64, a.v_tm, err) ||
+          make_map4(&mo, p.o, p.o_sb, p.o_sh, p.o_ld, p.B, p.H, p.Sq, 128, a.o_tm, err) ||
+          make_map4t(&mdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, p.dq, p.dq_sb, p.dq_sh, p.dq_ld, p.B, p.H, p.Sq, 32, 32,
+                     a.dq_tm, err))
+        return 1;
+      ProfScope prof_(c, "attn.bwd_dq");
+      const long items = (long)p.B * p.H * ((p.Sq + 127) / 128);   // persistent: one CTA per SM at most
+      const unsigned grid = (unsigned)(items < (long)c->sm_count ? items : (long)c->sm_count);
+      launch_pdl(c, attn_tc_dq_kernel, grid, kThreadsTC, smem_req(Q_SMEM), mq, mdo, mk, mv, mo, mdq, a);
+      if (check_launch("attn tc dq", err)) return 1;
+    }
   }
   if (want_dkdv) {
     CUtensorMap mk, mv, mq, mdo;
