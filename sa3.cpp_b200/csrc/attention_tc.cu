@@ -202,6 +202,20 @@ constexpr int smem_req(int bytes) { return bytes + 1024 > kSmemFloor ? bytes + 1
 constexpr int kThreadsTC = 32 * kWarpsTC;
 constexpr int NSTAGE = 4;
 
+// Work order of the grid-per-tile kernels and of the dq pass's items: every full tile of every
+// (b, h) first (the tiles of one (b, h) adjacent), then the (b, h)s' partial last tiles, so that
+// the short tiles fill the last round of SMs instead of being spread through it.  Linear index
+// L of nbh (b, h)s with `full` full tiles each (+ one partial when `part`) -> (bh, tile).
+__device__ __forceinline__ void heavy_first(int L, int nbh, int full, int& bh, int& tile) {
+  if (L < nbh * full) {
+    bh = L / full;
+    tile = L % full;
+  } else {
+    bh = L - nbh * full;
+    tile = full;
+  }
+}
+
 // ============================================================================== forward
 // CTA: two 128-query tiles of one (b, h) (warpgroup g: rows qbase + 128 g ..), key tiles of 64.
 // TMEM, per warpgroup at 256 g: S0, S1, S2 at [0, 64), [64, 128), [128, 192) (scores of three
@@ -231,8 +245,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int qbase = blockIdx.x * 256;
+  int bh, qt;
+  heavy_first((int)(blockIdx.y * gridDim.x + blockIdx.x), (int)gridDim.y, a.Sq / 256, bh, qt);
+  const int b = bh / a.H, h = bh % a.H;
+  const int qbase = qt * 256;
   const int ngrp = qbase + 128 < a.Sq ? 2 : 1;
   int kt0, kt1;
   tile_range(qbase, 128 * ngrp, a.Sk, a.window, 64, kt0, kt1);
@@ -471,8 +487,9 @@ struct ItemCursor {   // walks this CTA's items and their key tiles
   int item, nitems, step, qtiles, Sq, Sk, window, tile;
   int bh, r0, t0, t1;       // current item: (b, h), first row, visible other-side tile range
   __device__ __forceinline__ void load() {
-    bh = item / qtiles;
-    r0 = (item % qtiles) * 128;
+    int qt;
+    heavy_first(item, nitems / qtiles, Sq / 128, bh, qt);
+    r0 = qt * 128;
     tile_range(r0, 128, Sk, window, tile, t0, t1);
   }
   __device__ __forceinline__ bool valid() const { return item < nitems; }
@@ -824,8 +841,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, b = bh / a.H, h = bh % a.H;
-  const int k0 = blockIdx.x * 128;
+  int bh, kt;
+  heavy_first((int)(blockIdx.y * gridDim.x + blockIdx.x), (int)gridDim.y, a.Sk / 128, bh, kt);
+  const int b = bh / a.H, h = bh % a.H;
+  const int k0 = kt * 128;
   int qt0, qt1;
   tile_range(k0, 128, a.Sq, a.window, 64, qt0, qt1);
   const int nqt = qt1 - qt0;
