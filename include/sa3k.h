@@ -106,6 +106,14 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
  * Counterpart of the implicit sync in ggml_backend_tensor_get (src/train_loop.h:371). */
 int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len);
 
+/* Failure-path check of the bounded device waits (no counterpart in the reference).  Launches,
+ * on the context's stream, one kernel whose only wait is on a shared-memory barrier that nothing
+ * completes, bounded by limit_us microseconds (1 .. 2,000,000) through the same wait routine as
+ * every pipeline of this library.  The wait runs out, the kernel records the timeout in the
+ * context's device error word and returns: the next sa3k_sync reports "device wait timed out"
+ * and clears it, and the context stays usable.  Returns 0 when the kernel was launched. */
+int sa3k_check_bounded_wait(sa3k_ctx* ctx, int limit_us, char* err, int err_len);
+
 /* Per launch-class counters of this context: every kernel launch is counted by class
  * ("linear.fwd", "linear.dx", "lora.dA", "adamw", ...).  timing 1: each launch is also
  * bracketed by CUDA events on the context's stream and read sums the elapsed times.

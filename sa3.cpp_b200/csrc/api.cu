@@ -6,6 +6,7 @@
 #include "lora_kernels.h"
 #include "sa3k_internal.h"
 #include "materialize.h"
+#include "sa3k_common.cuh"
 
 #include <cmath>
 #include <cstdio>
@@ -277,6 +278,27 @@ int sa3k_sync(sa3k_ctx* ctx, char* err, int err_len) {
     cudaMemset(ctx->c.d_err, 0, sizeof(int));
     return fill_err(err, err_len, "device wait timed out inside a kernel (code " + std::to_string(code) + ")");
   }
+  return 0;
+}
+
+// One thread waits on a shared-memory mbarrier that nothing arrives at, through the same bounded
+// wait as every pipeline of the library: the wait runs out, records kErrTimeoutOther in the
+// context's error word and the kernel returns.
+__global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  sa3k::mbar_init(&bar, 1);
+  sa3k::fence_barrier_init();
+  sa3k::mbar_wait(&bar, 0u, err, sa3k::kErrTimeoutOther, limit_ns);
+}
+
+int sa3k_check_bounded_wait(sa3k_ctx* ctx, int limit_us, char* err, int err_len) {
+  if (!ctx) return fill_err(err, err_len, "ctx is NULL");
+  if (limit_us < 1 || limit_us > 2000000) return fill_err(err, err_len, "limit_us must be in 1 .. 2000000");
+  cudaSetDevice(ctx->c.device);
+  wait_probe_kernel<<<1, 32, 0, ctx->c.stream>>>(ctx->c.d_err, 1000ull * (unsigned long long)limit_us);
+  std::string e;
+  if (check_launch("wait probe", e)) return fill_err(err, err_len, e);
   return 0;
 }
 

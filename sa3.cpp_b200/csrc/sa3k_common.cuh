@@ -104,14 +104,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait for the barrier phase with the given parity to complete.  Returns false (and
-// records `code`) if it did not complete within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+// records `code`) if it did not complete within limit_ns (kWaitLimitNs unless given).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = globaltimer();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+    if ((i & 63u) == 0 && globaltimer() - t0 > limit_ns) {
       record_error(err, code);
       return false;
     }

@@ -17,7 +17,7 @@ TYPE_IDS = {"f32": 0, "f16": 1, "q8_0": 8, "q4_k": 12}
 
 # every symbol include/sa3k.h declares
 ABI_SYMBOLS = (
-    "sa3k_version", "sa3k_ctx_create", "sa3k_ctx_destroy", "sa3k_ctx_set_stream", "sa3k_sync",
+    "sa3k_version", "sa3k_ctx_create", "sa3k_ctx_destroy", "sa3k_ctx_set_stream", "sa3k_sync", "sa3k_check_bounded_wait",
     "sa3k_weight_upload", "sa3k_weight_free", "sa3k_dequant", "sa3k_row_norms", "sa3k_col_norms", "sa3k_linear_fwd",
     "sa3k_linear_bwd", "sa3k_linear_fwd_bwd", "sa3k_linear_fwd_bwd_host", "sa3k_adamw",
     "sa3k_average_clip_adamw", "sa3k_profile_enable", "sa3k_profile_read", "sa3k_ctx_set_option",
@@ -127,6 +127,7 @@ def lib():
         L.sa3k_ctx_destroy.restype = None
         L.sa3k_ctx_set_stream.argtypes = [P, P, E, I]
         L.sa3k_sync.argtypes = [P, E, I]
+        L.sa3k_check_bounded_wait.argtypes = [P, I, E, I]
         L.sa3k_weight_upload.argtypes = [P, I, P, I64, I64, ctypes.POINTER(P), E, I]
         L.sa3k_weight_free.argtypes = [P]
         L.sa3k_weight_free.restype = None
@@ -241,6 +242,12 @@ class Context:
     def sync(self):
         err = ctypes.create_string_buffer(512)
         _check(lib().sa3k_sync(self._h, err, 512), err)
+
+    def check_bounded_wait(self, limit_us):
+        """Launch the bounded-wait probe (a wait that runs out after limit_us); the next sync()
+        raises with the timeout."""
+        err = ctypes.create_string_buffer(512)
+        _check(lib().sa3k_check_bounded_wait(self._h, int(limit_us), err, 512), err)
 
     def _own(self, obj):
         """Objects made on this context (weights, models, communicators) are released before it."""
