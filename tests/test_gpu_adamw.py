@@ -58,3 +58,27 @@ def test_average_clip_adamw(ctx, count, clip):
     np.testing.assert_allclose(p.cpu().numpy(), rp, rtol=1e-6, atol=1e-4 * 1e-5)
     np.testing.assert_allclose(m.cpu().numpy(), rm, rtol=1e-6, atol=0)
     assert np.array_equal(gd.cpu().numpy(), grad)      # the accumulated gradient is left untouched
+
+
+def test_adamw_vector_and_scalar_paths_agree(ctx):
+    """16-byte aligned buffers take the four-wide kernel (plus a scalar tail), misaligned views
+    the scalar one: both apply the same per-element arithmetic, so the results are identical."""
+    import torch
+    import sa3k
+    rng = np.random.default_rng(5)
+    n = 4099
+    p0 = rng.normal(0, 0.05, n).astype(np.float32)
+    grad = rng.normal(0, 0.1, n).astype(np.float32)
+    hp = sa3k.AdamWParams(1e-3, 0.9, 0.999, 1e-8, 0.01, 0.0)
+    out = []
+    for off in (0, 1):
+        bufs = [torch.zeros(n + 1, device="cuda") for _ in range(4)]
+        p, gr, m, v = (b[off:off + n] for b in bufs)
+        p.copy_(torch.from_numpy(p0))
+        gr.copy_(torch.from_numpy(grad))
+        for step in (1, 2):
+            ctx.adamw(p, gr, m, v, hp, step)
+        ctx.sync()
+        out.append([t.cpu().numpy().view(np.uint32) for t in (p, m, v)])
+    for a, b in zip(out[0], out[1]):
+        assert np.array_equal(a, b)
