@@ -99,6 +99,12 @@ int sa3k_ctx_set_stream(sa3k_ctx* ctx, void* cuda_stream, char* err, int err_len
  *       Q8_0, half for Q4_K).  0: dequantize into a shared-memory B tile instead.  Results are
  *       identical up to the order of the f32 accumulation. */
 #define SA3K_OPT_DEQUANT_TMEM 8
+/* SA3K_OPT_FUSE_HEAD_PREP  1 (default): in the DiT step, the self-attention q / k head preparation
+ *       (per-head RMS norm, NeoX RoPE) runs in the epilogue of the qkv projection GEMM whenever that
+ *       GEMM takes the CTA-pair kernel with an f16 weight operand (no differential slices).  0: a
+ *       separate pass over the projection output.  The two differ only in the rounding of the
+ *       projection output before the norm (f32 in the epilogue, f16 in the separate pass). */
+#define SA3K_OPT_FUSE_HEAD_PREP 9
 int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int err_len);
 
 /* Wait for the context's stream and report any asynchronous or device-side error (a bounded

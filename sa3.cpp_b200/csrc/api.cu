@@ -262,6 +262,7 @@ int sa3k_ctx_set_option(sa3k_ctx* ctx, int option, int64_t value, char* err, int
     case SA3K_OPT_PDL: ctx->c.pdl = value != 0; return 0;
     case SA3K_OPT_STEP_GRAPH: ctx->c.step_graph = value != 0; return 0;
     case SA3K_OPT_DEQUANT_TMEM: ctx->c.dequant_tmem = value != 0; return 0;
+    case SA3K_OPT_FUSE_HEAD_PREP: ctx->c.fuse_head_prep = value != 0; return 0;
     default: return fill_err(err, err_len, "unknown option");
   }
 }

@@ -56,6 +56,9 @@ struct HeadSlice {
   int rope = 0;           // apply RoPE after the norm
   float* rstd = nullptr;  // [T][H] saved for the backward (norm slices)
 };
+// NeoX RoPE (cos, sin) table [tps][rot / 2] of the context (null when rot == 0), followed by the
+// same values frequency-major, [rot / 2][tps]
+const float2* k_rope_table(Ctx* c, int tps, int rot, float rope_base, std::string& err);
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
                     int tokens_per_sample, float eps, int rot, float rope_base, __half* out, std::string& err);
 // the same with f16 projection rows

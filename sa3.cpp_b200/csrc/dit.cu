@@ -451,7 +451,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
 
 // ------------------------------------------------------------------ linear helpers
 static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float* bias, const __half* x,
-                   int64_t M, float* y, __half* y_h, std::string& err) {
+                   int64_t M, float* y, __half* y_h, std::string& err, const HeadPrepEpi* hp = nullptr) {
   if (t && t->mat) {
     if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
     GemmDesc g;   // y = x W_eff^T + bias
@@ -466,6 +466,7 @@ static int lin_fwd(DitModel& m, const Weight* w, const DitTarget* t, const float
   }
   LinearFwd f;
   f.w = w; f.ad = t ? &t->prep : nullptr; f.bias = bias; f.x_h = x; f.M = M; f.y = y; f.y_h = y_h;
+  f.hp = hp;
   if (t) {
     if (t->rows != M || t->x_h != x) { err = "adapter " + t->name + " bound to other input rows"; return 1; }
     f.ut = t->ut; f.ut_ld = t->ut_ld;
@@ -559,15 +560,16 @@ static __half* dz_of(DitModel& m, const DitTarget* t) {
 }
 static float* dg_of(DitModel& m, const DitTarget* t) { return t && !t->mat && m.r16_grads.table ? t->dg : m.dg; }
 
-// self-attention of block `a` over the prepared [q | k | v (| qd | kd)] rows: softmax stream 0
-// (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] f16
+// self-attention of block `a` over the prepared [q | k | . (| qd | kd)] rows: softmax stream 0
+// (q, k) or the differential stream 1 (qd, kd), both on v, output o [M][D] f16.  v takes no
+// preparation and is read from the projection output itself.
 static AttnArgs self_attn(const DitBlockAct& a, int B, int H, int S, int D, int Q, float scale, int st,
                           __half* o) {
   AttnArgs r;
   r.B = B; r.H = H; r.Sq = S; r.Sk = S; r.scale = scale; r.window = -1;
   r.q = a.qkvb + (st ? 3 * D : 0); r.q_sb = (long)S * Q; r.q_sh = 64; r.q_ld = Q;
   r.k = a.qkvb + (st ? 4 * D : D); r.k_sb = r.q_sb; r.k_sh = 64; r.k_ld = Q;
-  r.v = a.qkvb + 2 * D; r.v_sb = r.q_sb; r.v_sh = 64; r.v_ld = Q;
+  r.v = a.qkv + 2 * D; r.v_sb = r.q_sb; r.v_sh = 64; r.v_ld = Q;
   r.o = o; r.o_sb = (long)S * D; r.o_sh = 64; r.o_ld = D;
   r.lse = st ? a.lse_a2 : a.lse_a;
   return r;
@@ -684,17 +686,34 @@ static int dit_step(DitModel& m, std::string& err) {
     if (l == 0 &&
         k_rmsnorm_mod_fwd(c, a.x, (int)M, D, g_pre, a.mod, a.mod + D, ms, S, k.norm_eps, a.h_a, a.rstd_a, err))
       return 1;
+    // the q / k head preparation (RMS norm, RoPE) runs in the epilogue of the qkv GEMM when that
+    // GEMM takes the CTA-pair kernel with the f16 weight operand (no differential slices, no
+    // materialized qkv target); otherwise as its own pass over the projection output
+    const bool f16_w = wqkv->type == kTypeF16 || wqkv->type == kTypeF32 || (wqkv->f16 && !c->smem_dequant);
+    const bool fuse_hp = !diff && (k.rot == 0 || k.rot == 32 || k.rot == 64) && !(tq && tq->mat) && f16_w &&
+                         c->fuse_head_prep && gemm_pair_applies(c, (int)M, Q, true);
+    if (fuse_hp) {
+      HeadPrepEpi hp;
+      hp.out = a.qkvb; hp.ld = Q;
+      hp.gq = g_q; hp.gk = g_k; hp.rq = a.rq; hp.rk = a.rk;
+      hp.tab = k.rot ? k_rope_table(c, S, k.rot, k.rope_base, err) : nullptr;
+      if (k.rot && !hp.tab) return 1;
+      if (hp.tab) hp.tab += (long)S * (k.rot / 2);   // the frequency-major copy
+      hp.tps = S; hp.rot = k.rot; hp.D = D; hp.H = H; hp.eps = k.qk_eps;
+      if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, nullptr, a.qkv, err, &hp)) return 1;
+    } else {
     if (lin_fwd(m, wqkv, tq, nullptr, a.h_a, M, nullptr, a.qkv, err)) return 1;
     {
-      // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE
-      HeadSlice hs[5];
+      // [q | k | v (| qd | kd)]: q / qd share q_norm, k / kd share k_norm, all four take RoPE;
+      // v is left where the projection wrote it
+      HeadSlice hs[4];
       hs[0].col = 0; hs[0].gamma = g_q; hs[0].rope = 1; hs[0].rstd = a.rq;
       hs[1].col = D; hs[1].gamma = g_k; hs[1].rope = 1; hs[1].rstd = a.rk;
-      hs[2].col = 2 * D;
-      hs[3].col = 3 * D; hs[3].gamma = g_q; hs[3].rope = 1; hs[3].rstd = a.rq2;
-      hs[4].col = 4 * D; hs[4].gamma = g_k; hs[4].rope = 1; hs[4].rstd = a.rk2;
-      if (k_head_prep_fwd(c, a.qkv, (int)M, Q, H, hs, diff ? 5 : 3, S, k.qk_eps, k.rot, k.rope_base, a.qkvb, err))
+      hs[2].col = 3 * D; hs[2].gamma = g_q; hs[2].rope = 1; hs[2].rstd = a.rq2;
+      hs[3].col = 4 * D; hs[3].gamma = g_k; hs[3].rope = 1; hs[3].rstd = a.rk2;
+      if (k_head_prep_fwd(c, a.qkv, (int)M, Q, H, hs, diff ? 4 : 2, S, k.qk_eps, k.rot, k.rope_base, a.qkvb, err))
         return 1;
+    }
     }
     AttnArgs sa = self_attn(a, B, H, S, D, Q, scale, 0, diff ? a.o1 : a.oa);
     if (attn_forward(c, sa, err)) return 1;

@@ -17,15 +17,19 @@ namespace {
 
 // RoPE angle of pair i (< rot/2) at position pos: pos * base^(-2i/rot); its (cos, sin) come from
 // a table built once per (positions, rot, base) rather than from sincos in every warp.
+// (cos, sin) of NeoX RoPE, twice: position-major tab[pos * half + i] (the head-preparation
+// kernels, 8 lanes per row) and frequency-major tab[n + i * tps + pos] (the GEMM epilogue, one
+// row per lane: consecutive lanes read consecutive positions)
 __global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __restrict__ tab) {
-  const int half = rot / 2;
+  const int half = rot / 2, n = tps * half;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= tps * half) return;
+  if (e >= n) return;
   const int pos = e / half, i = e % half;
   const float freq = exp2f(-2.0f * (float)i / (float)rot * log2_base);
   float sn, cs;
   sincosf((float)pos * freq, &sn, &cs);
   tab[e] = make_float2(cs, sn);
+  tab[n + (long)i * tps + pos] = make_float2(cs, sn);
 }
 
 // Head preparation kernels: 8 lanes per head row.  Lane l of a warp: row group q = l >> 3 (four
@@ -747,9 +751,9 @@ int k_rmsnorm_mod_bwd(Ctx* c, const float* dh, const float* x, const float* rstd
 }
 
 // (cos, sin) table of the context for (tps, rot, base); rebuilt only when one of them changes
-static const float2* rope_table(Ctx* c, int tps, int rot, float rope_base, std::string& err) {
+const float2* k_rope_table(Ctx* c, int tps, int rot, float rope_base, std::string& err) {
   if (rot == 0) return nullptr;
-  const size_t bytes = sizeof(float2) * (size_t)tps * (rot / 2);
+  const size_t bytes = 2 * sizeof(float2) * (size_t)tps * (rot / 2);
   void* tab = scratch_get(c, kSlotRope, bytes, err);
   if (!tab) return nullptr;
   if (tab != c->rope_tab || c->rope_tps != tps || c->rope_rot != rot || c->rope_base != rope_base) {
@@ -783,7 +787,7 @@ static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const He
   }
   hs.n = nslices;
   const float2* tab = nullptr;
-  if (any_rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
+  if (any_rope && rot && !(tab = k_rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
@@ -806,7 +810,7 @@ int k_qkv_bwd_dz(Ctx* c, const float* dq3, const __half* qkv, int T, int D, int 
                  int tps, int rot, float rope_base, const float* g, __half* dz, float* dg, std::string& err) {
   if (nsl != 3 && nsl != 5) { err = "qkv backward: 3 or 5 slices"; return 1; }
   const float2* tab = nullptr;
-  if (rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
+  if (rot && !(tab = k_rope_table(c, tps, rot, rope_base, err))) return 1;
   if ((T + kQkvRows - 1) / kQkvRows > 65535) { err = "qkv backward: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * nsl * D, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "qkv_bwd_dz");
@@ -819,7 +823,7 @@ int k_head_prep_bwd(Ctx* c, const float* g, long g_ld, const float* y, int T, in
                     int tps, int rot, float rope_base, float* dy, __half* dy_h, std::string& err,
                     float gscale, const float* g2, long g2_ld) {
   const float2* tab = nullptr;
-  if (sl.rope && rot && !(tab = rope_table(c, tps, rot, rope_base, err))) return 1;
+  if (sl.rope && rot && !(tab = k_rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_bwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
   const dim3 grid((unsigned)((H + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));

@@ -230,6 +230,10 @@ static int launch_pair(Ctx* c, const GemmDesc& d, const CUtensorMap& ta, const C
              !make_map(&tout, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, d.out_h, d.N, d.M, d.ldo_h * 2, 64, 32, SW, "out_h", e2))
       a.tma_out = 2;
   }
+  if (d.hp && (a.tma_out != 2 || d.N != 3 * d.hp->D || d.hp->D % 64)) {
+    err = "gemm: the fused head preparation needs an aligned row-major f16 output of [q | k | v]";
+    return 1;
+  }
   const long tiles = (long)((d.M + 2 * kBM - 1) / (2 * kBM)) * ((d.N + BN - 1) / BN);
   if (plan_tail(c, d, a, tiles, (long)max_clusters, (d.M + 2 * kBM - 1) / (2 * kBM), BN, err)) return 1;
   const long items = a.tail_parts > 1 ? a.tail_t0 + (tiles - a.tail_t0) * a.tail_parts : tiles;
@@ -332,6 +336,15 @@ static bool wq_fits(const GemmDesc& d) {
   return !d.a_mn && code_ld % 16 == 0 && (!q4 || d.bsrc == kB_WEIGHT_NT || w->out % 2 == 0);
 }
 
+bool gemm_pair_applies(const Ctx* c, int M, int N, bool f16_b) {
+  if (!c->gemm_pair || !f16_b || M < 2 * kBM || N < 256) return false;
+  if (c->gemm_pair == 2) return true;
+  if (c->tile_n != 0) return false;
+  const long clusters = (long)(c->sm_count / 2);
+  const long tm2 = (M + 2 * kBM - 1) / (2 * kBM);
+  return tm2 * ((N + 255) / 256) >= clusters;
+}
+
 int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   if (d.M <= 0 || d.N <= 0 || d.K < 0 || (d.K == 0 && !d.ext_at)) {
     err = "gemm: need M, N > 0 and K > 0";
@@ -342,6 +355,7 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   // and the context has not asked for the in-smem path explicitly
   const bool quant = weight_b && d.w && (d.w->type == kTypeQ8_0 || d.w->type == kTypeQ4_K) &&
                      !(d.w->f16 && !c->smem_dequant);
+  if (d.hp && quant) { err = "gemm: the fused head preparation needs an f16 weight operand"; return 1; }
   if (quant && c->dequant_tmem && wq_fits(d)) {
     // (inside a stream capture the transposed codes of an input-gradient GEMM cannot be made: such
     // a GEMM keeps to the shared-memory dequant path until an eager call has made them)
@@ -443,6 +457,8 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
   a.partial = nullptr;
   a.tma_out = 0;
   a.atomic = 0;
+  a.has_hp = d.hp ? 1 : 0;
+  if (d.hp) a.hp = *d.hp;
 
   if (bn == 16) {
     if (bmode != 0) { err = "gemm: N tile 16 supports f16 K-major B only"; return 1; }
@@ -481,11 +497,13 @@ int gemm(Ctx* c, const GemmDesc& d, std::string& err) {
       if (d.ext_at) {
         if (make_map(&teb2, BF, d.ext_b, 64, d.N, 128, 64, bp / 2, SW, "ext B half", err)) return 1;
       }
+      if (d.hp && bmode != 0) { err = "gemm: the fused head preparation needs a K-major B operand"; return 1; }
       if (bp == 192) return launch_pair<192, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err);
       return bmode == 0 ? launch_pair<256, 6, 0>(c, d, ta, tb2, tea2, teb2, a, err)
                         : launch_pair<256, 6, 1>(c, d, ta, tb2, tea2, teb2, a, err);
     }
   }
+  if (d.hp) { err = "gemm: the fused head preparation runs on the CTA-pair kernel only"; return 1; }
   if (bn == 256) {
     switch (bmode) {
       case 0: return launch<256, 4, 0, false>(c, d, ta, tb, tbs, tea, teb, a, err);

@@ -30,6 +30,7 @@
 #pragma once
 
 #include "sa3k_common.cuh"
+#include "sa3k_internal.h"
 
 namespace sa3k {
 
@@ -60,6 +61,8 @@ struct GemmArgs {
   int tma_out;              // 1: f32 `out` via TMA store / reduce-add; 2: f16 `out_h` via TMA
                             //    store; 0: direct stores (split-K partials, transposed or dual outputs)
   int atomic;               // split-K: every split adds its (scaled) part into `out` with atomics
+  int has_hp;               // the fused head preparation below applies (CTA-pair kernel)
+  HeadPrepEpi hp;
   int* err;                 // device error word
 };
 

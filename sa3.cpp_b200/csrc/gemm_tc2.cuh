@@ -94,6 +94,50 @@ __device__ __forceinline__ void umma_commit_pair_w(uint64_t* bar) {
       : "memory");
 }
 
+// NeoX rotation of the first 2 HALF dims of a head: dims i and i + HALF rotate together by the
+// (cos, sin) pair cs[i * tps] of the row's position (frequency-major table, so the lanes of a warp,
+// on consecutive rows, read consecutive pairs)
+template <int HALF>
+__device__ __forceinline__ void head_rope(float (&v)[64], const float2* cs, int tps) {
+#pragma unroll
+  for (int i = 0; i < HALF; ++i) {
+    const float2 t = __ldg(cs + (long)i * tps);
+    const float a = v[i], b = v[i + HALF];
+    v[i] = a * t.x - b * t.y;
+    v[i + HALF] = b * t.x + a * t.y;
+  }
+}
+
+// The fused head preparation of one 64-column head of `row` (HeadPrepEpi): f holds the GEMM's
+// f32 values of columns nb .. nb + 63.  q and k heads only: v is read from the GEMM's own output.
+__device__ __forceinline__ void head_prep_epi(const HeadPrepEpi& p, const float* f, int nb, int row) {
+  const int slice = nb / p.D, h = (nb - slice * p.D) >> 6;
+  if (slice >= 2) return;
+  float v[64];
+#pragma unroll
+  for (int k = 0; k < 64; ++k) v[k] = f[k];
+  {
+    const float* gm = slice == 0 ? p.gq : p.gk;
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 64; ++k) ss = fmaf(v[k], v[k], ss);
+    const float r = rsqrtf(ss / 64.f + p.eps);
+    (slice == 0 ? p.rq : p.rk)[(long)row * p.H + h] = r;
+#pragma unroll
+    for (int k = 0; k < 64; k += 4) {
+      const float4 g4 = __ldg(reinterpret_cast<const float4*>(gm + k));
+      v[k] *= r * g4.x; v[k + 1] *= r * g4.y; v[k + 2] *= r * g4.z; v[k + 3] *= r * g4.w;
+    }
+    if (p.tab && p.rot == 32) head_rope<16>(v, p.tab + row % p.tps, p.tps);
+    else if (p.tab && p.rot == 64) head_rope<32>(v, p.tab + row % p.tps, p.tps);
+  }
+  uint4* dst = reinterpret_cast<uint4*>(p.out + (long)row * p.ld + nb);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    dst[c] = make_uint4(pack_f16x2(v[8 * c], v[8 * c + 1]), pack_f16x2(v[8 * c + 2], v[8 * c + 3]),
+                        pack_f16x2(v[8 * c + 4], v[8 * c + 5]), pack_f16x2(v[8 * c + 6], v[8 * c + 7]));
+}
+
 constexpr int kPairEpiWarps = 8;        // two per TMEM lane quarter, alternate column chunks
 constexpr int kPairThreads = 32 * (2 + kPairEpiWarps);
 
@@ -307,6 +351,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           epi_columns(v, f + 32 * h, nb + 32 * h, args, false, bias);
         }
         if (!have || nb >= args.N) continue;
+        if (args.has_hp && rbase + lane < args.M) head_prep_epi(args.hp, f, nb, rbase + lane);   // (cstep is 64)
         if (args.tma_out) {
           uint8_t* buf = stg + (L::STAGE_BUFS == 2 ? (nstore & 1) : 0) * L::STAGE_BYTES;
           if (nstore >= L::STAGE_BUFS) {

@@ -92,6 +92,7 @@ int linear_forward(Ctx* c, const LinearFwd& f, std::string& err) {
   g.col_bias = f.bias;
   g.out = f.y; g.ldo = w->out;
   g.out_h = f.y_h; g.ldo_h = w->out;
+  g.hp = f.hp;
   g.name = "linear.fwd";
   return gemm(c, g, err);
 }

@@ -46,6 +46,7 @@ struct LinearFwd {
   // adapter scratch: ut [16][ut_ld] f16 (u^T: the K = 16 extension operand, kept for backward)
   __half* ut = nullptr;
   int64_t ut_ld = 0;
+  const HeadPrepEpi* hp = nullptr;     // fused head preparation of a qkv projection (see gemm())
 };
 int linear_forward(Ctx* c, const LinearFwd& f, std::string& err);
 // u = x A^T of an adapter, written as ut = f16(u)^T [16][ut_ld]

@@ -65,6 +65,7 @@ struct Ctx {
   bool pdl = true;                   // programmatic dependent launch between consecutive kernels
   bool step_graph = true;            // the DiT step records and replays a CUDA graph
   bool dequant_tmem = true;          // in-kernel dequantization into tensor memory (gemm_wq)
+  bool fuse_head_prep = true;        // DiT: q / k head preparation in the qkv GEMM's epilogue
   // bumped whenever something a recorded graph may depend on changes: an option, a scratch
   // buffer reallocated, the RoPE table rebuilt
   uint64_t gen = 0;
@@ -156,6 +157,23 @@ enum BSource : int {
   kB_WEIGHT_TN = 3,     // weight W[out = K][in = N], used as W^T (dx = dy W)
 };
 
+// Head preparation fused into the epilogue of a self-attention qkv projection (the CTA-pair GEMM
+// with an f16 output): for output columns [0, 2 D) (q and k) each 64-column head gets its RMS
+// norm (gq / gk, rstd stored to rq / rk [M][H]) and then the NeoX rotation of its first rot dims
+// at the row's position (row % tps); columns [2 D, 3 D) (v) are copied.  The prepared heads go to
+// `out` [M][ld] f16; the GEMM's own f16 output keeps the values before preparation.
+struct HeadPrepEpi {
+  __half* out = nullptr;
+  long ld = 0;
+  const float* gq = nullptr;
+  const float* gk = nullptr;
+  float* rq = nullptr;
+  float* rk = nullptr;
+  const float2* tab = nullptr;   // [rot / 2][tps] (cos, sin), frequency-major; null: no rotation
+  int tps = 0, rot = 0, D = 0, H = 0;
+  float eps = 0.f;
+};
+
 struct GemmDesc {
   int M = 0, N = 0, K = 0;
   // A: f16, K-major [M][lda] or (a_mn) MN-major [K][lda]
@@ -190,10 +208,13 @@ struct GemmDesc {
   // split-K partial sums may be added into `out` with f32 atomics (no reduction pass; the
   // summation order, and so the last bits, vary from run to run).  f32 `out` only.
   int atomic_split = 0;
+  const HeadPrepEpi* hp = nullptr;   // fused head preparation (CTA-pair path, f16 output only)
   const char* name = "gemm";   // launch class for the profiler
 };
 
 int gemm(Ctx* c, const GemmDesc& d, std::string& err);
+// true when gemm() runs an M x N GEMM with an f16 B operand (f16_b) on the CTA-pair kernel
+bool gemm_pair_applies(const Ctx* c, int M, int N, bool f16_b);
 
 }  // namespace sa3k
 

@@ -35,6 +35,7 @@ ABI_SYMBOLS = (
 OPT_WEIGHT_F16_CACHE, OPT_SMEM_DEQUANT, OPT_GEMM_TILE_N, OPT_GEMM_PAIR, OPT_ATTN_TC, OPT_PDL = 1, 2, 3, 4, 5, 6
 OPT_STEP_GRAPH = 7
 OPT_DEQUANT_TMEM = 8
+OPT_FUSE_HEAD_PREP = 9
 
 
 class Sa3kError(RuntimeError):
