@@ -435,8 +435,10 @@ def dit_row_kernel_bytes(cfg, B, T, C):
         "residual_norm": 14.0 * M * D * 3,
         # dh, x, gx in; gx out (f32); the feed-forward norm also writes gx as f16
         "rmsnorm_mod_bwd": 16.0 * M * D * 3 + 2.0 * M * D,
-        # qkv f16 in / out; cross q f32 in, f16 out; cross kv (context rows) f32 in, f16 out
-        "head_prep_fwd": 4.0 * M * Q * D + 6.0 * M * D + 12.0 * MC * D,
+        # cross q f32 in, f16 out; cross kv (context rows) f32 in, f16 out; the self-attention q / k
+        # are prepared in the qkv GEMM's epilogue, except with differential attention, whose
+        # q, k, qd, kd (f16 in / out) take this pass
+        "head_prep_fwd": (16.0 * M * D if Q == 5 else 0.0) + 6.0 * M * D + 12.0 * MC * D,
         # cross q gradient (f32) and its f32 projection output in, f16 dz out
         "head_prep_bwd": 10.0 * M * D,
         # attention gradients (f32) and qkv (f16) in, dz (f16) out
