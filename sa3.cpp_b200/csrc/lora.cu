@@ -210,10 +210,12 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
 
 // SwiGLU backward (src/dit.h:259-264): f[t] = [val | gate] is the ff.proj output (f16), da (f16)
 // the gradient of val * silu(gate); dy = [d val | d gate] is the ff.proj output gradient (2I
-// columns).  Thread = 8 columns of val and the matching 8 of gate (16-byte loads and stores),
-// block = kFuseTok rows, kSwiRows rows' loads issued at a time; dz = f16(g dy) and, for DoRA,
-// dg += colsum(dy (y - bias) / g) with the reciprocals of g taken once per thread.
+// columns).  Thread = 8 columns of val and the matching 8 of gate (16-byte loads and stores);
+// the blocks walk chunks of kSwiRows rows grid-stride (every row's loads of a chunk issued
+// first), with a grid of kSwiBlocks blocks per SM, so no partial last wave is left; dz = f16(g dy)
+// and, for DoRA, dg += colsum(dy (y - bias) / g) with the reciprocals of g taken once per thread.
 constexpr int kSwiRows = 4;
+constexpr int kSwiBlocks = 4;
 
 __device__ __forceinline__ void f16x8(const uint4 w, float (&v)[8]) {
   const uint32_t u[4] = {w.x, w.y, w.z, w.w};
@@ -234,14 +236,13 @@ __device__ __forceinline__ uint4 f16x8_pack(const float (&v)[8]) {
   return make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]));
 }
 
-__global__ void swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half* __restrict__ f, int T,
-                                     int I,
-                                     const float* __restrict__ bias, const float* __restrict__ g,
-                                     __half* __restrict__ dz, float* __restrict__ dg) {
+__global__ void __launch_bounds__(128, kSwiBlocks)
+    swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half* __restrict__ f, int T, int I,
+                         const float* __restrict__ bias, const float* __restrict__ g, __half* __restrict__ dz,
+                         float* __restrict__ dg) {
   pdl_prologue();
   const int j = 8 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (j >= I) return;
-  const int t0 = blockIdx.y * kFuseTok, t1 = min(T, t0 + kFuseTok);
   const bool dora = g != nullptr;
   float gv[8], gg[8], igv[8], igg[8], bv[8], bg[8];
 #pragma unroll
@@ -259,7 +260,8 @@ __global__ void swiglu_bwd_dz_kernel(const __half* __restrict__ da, const __half
   float accv[8], accg[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) accv[e] = accg[e] = 0.f;
-  for (int tb = t0; tb < t1; tb += kSwiRows) {
+  for (int tb = blockIdx.y * kSwiRows; tb < T; tb += gridDim.y * kSwiRows) {
+    const int t1 = min(T, tb + kSwiRows);
     uint4 v4[kSwiRows], g4[kSwiRows], d4[kSwiRows];
 #pragma unroll
     for (int u = 0; u < kSwiRows; ++u) {             // every row's loads first
@@ -595,11 +597,11 @@ int k_swiglu_bwd_dz(Ctx* c, const __half* da, const __half* f, int T, int I, con
                     const float* g,
                     __half* dz, float* dg, std::string& err) {
   if (I % 8) { err = "swiglu: the hidden width must be a multiple of 8"; return 1; }
-  if ((T + kFuseTok - 1) / kFuseTok > 65535) { err = "swiglu: too many rows"; return 1; }
   if (g && cudaMemsetAsync(dg, 0, sizeof(float) * 2 * I, c->stream) != cudaSuccess) return check_launch("memset", err);
   ProfScope prof_(c, "swiglu_bwd_dz");
-  launch_pdl(c, swiglu_bwd_dz_kernel, dim3((unsigned)((I / 8 + 127) / 128), (unsigned)((T + kFuseTok - 1) / kFuseTok)),
-             128, 0, da, f, T, I, bias, g, dz, dg);
+  const unsigned gx = (unsigned)((I / 8 + 127) / 128), nchunk = (unsigned)((T + kSwiRows - 1) / kSwiRows);
+  const unsigned gy = std::max(1u, std::min(nchunk, (unsigned)(kSwiBlocks * c->sm_count) / gx));
+  launch_pdl(c, swiglu_bwd_dz_kernel, dim3(gx, gy), 128, 0, da, f, T, I, bias, g, dz, dg);
   return check_launch("swiglu_bwd_dz", err);
 }
 
