@@ -201,6 +201,42 @@ def test_fused_and_separate_head_preparation_agree(ctx):
     assert worst < 2e-3, worst
 
 
+def test_fused_head_preparation_full_rotation(ctx):
+    """The fused epilogue's other RoPE width, the whole head (rot 64), at width 512 (8 heads, one
+    block) with CTA pairs forced wherever they apply, so the qkv GEMM takes the pair kernel and its
+    epilogue; compared with the separate head-preparation pass as above."""
+    import sa3k
+    rot = 64
+    cfg = dict(CFG, dim=512, heads=8, depth=1, ff_inner=2048, rot=rot)
+    dit, deq, ad, targets, rng = _build(ctx, cfg, seed=23 + rot)
+    inputs = _inputs(rng, cfg)
+    out = []
+    ctx.set_option(sa3k.OPT_GEMM_PAIR, 2)
+    try:
+        for fused in (1, 0):
+            ctx.set_option(sa3k.OPT_FUSE_HEAD_PREP, fused)
+            dit.zero_grads()
+            loss = np.zeros(B, np.float32)
+            dit.forward_backward(B, T, CTX, *inputs, loss=loss)
+            ctx.sync()
+            grads = np.zeros(dit.size(), np.float32)
+            dit.copy(1, grads, to_model=False)
+            out.append((loss, grads))
+    finally:
+        ctx.set_option(sa3k.OPT_FUSE_HEAD_PREP, 1)
+        ctx.set_option(sa3k.OPT_GEMM_PAIR, 1)
+        dit.close()
+    (l1, g1), (l0, g0) = out
+    assert np.max(np.abs(l1 - l0) / np.abs(l0)) < 5e-4, (l1, l0)
+    worst = 0.0
+    for name in targets:
+        oa, ob, om = ad[name]["offs"]
+        for off, n in ((oa, ad[name]["A"].size), (ob, ad[name]["B"].size), (om, ad[name]["m"].size)):
+            worst = max(worst, rel_l2(g1[off:off + n], g0[off:off + n]))
+    print(f"\n[fused vs separate head preparation, rot {rot}] worst gradient rel-L2 {worst:.3g}")
+    assert worst < 2e-3, worst
+
+
 def test_distance_to_ggml_cpu_numerics(ctx):
     """Reported, not gated: how far the GPU step's adapter gradients lie from the oracle in mode (ii),
     the activation rounding of ggml's CPU backend over a Q8_0 base (every frozen linear's input
