@@ -84,6 +84,7 @@ struct DitBlockAct {
   __half *o1 = nullptr, *o2 = nullptr, *oc1 = nullptr, *oc2 = nullptr;
   float *lse_a2 = nullptr, *lse_c2 = nullptr, *rq2 = nullptr, *rk2 = nullptr, *rcq2 = nullptr, *rck2 = nullptr;
   float* yc = nullptr;   // cross.out output, kept when that linear has an adapter
+  int64_t kv_ld = 0;     // row stride of kvf / kvb (depth x their width when the blocks share them)
 };
 
 struct DitModel {
@@ -160,6 +161,15 @@ struct DitModel {
   float *dgcond = nullptr, *dgsum = nullptr, *dxin0 = nullptr, *dxp = nullptr;
   bool need_ctx = false, need_mod = false, need_x0 = false;
   __half *dO_b = nullptr, *dact_b = nullptr;   // dact_b: the SwiGLU output gradient, f16
+  // the context K / V projections of every block as one GEMM (no adapter on any cross.kv, nothing
+  // differentiated through them): the blocks' f16 weights stacked [depth x Dk][dim], refilled when
+  // the model generation changes; the outputs kvf_all (f32) / kvb_all (prepared, f16) are
+  // [MC][depth x Dk], block l at column l Dk
+  bool kv_batched = false;
+  __half* kv_w_all = nullptr;
+  uint64_t kvw_mgen = ~0ull;
+  float* kvf_all = nullptr;
+  __half* kvb_all = nullptr;
   // linear scratch
   float *dg = nullptr, *c3 = nullptr;
   __half *dut = nullptr, *dz = nullptr, *cb = nullptr;
@@ -352,6 +362,8 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
   m.need_mod = has_target(m, "time_embed.") || has_target(m, "global_embed.") || has_target(m, ".gce.");
   m.need_x0 = has_target(m, "pre_conv.") || has_target(m, "proj_in.");
   const bool any_cq = has_target(m, ".cross.q."), need_kv = m.need_ctx || has_target(m, ".cross.kv.");
+  m.kv_batched = !need_kv && k.depth > 1;
+  const int64_t kv_ld = m.kv_batched ? (int64_t)k.depth * Dk : Dk;
   // two passes: measure, then carve
   for (int pass = 0; pass < 2; ++pass) {
     char* base = static_cast<char*>(m.arena);
@@ -363,13 +375,22 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     };
     auto f = [&](int64_t n) { return static_cast<float*>(take(n * 4)); };
     auto h = [&](int64_t n) { return static_cast<__half*>(take(n * 2)); };
+    m.kvf_all = m.kv_batched ? f(MC * kv_ld) : nullptr;
+    m.kvb_all = m.kv_batched ? h(MC * kv_ld) : nullptr;
     m.blk.assign(k.depth, DitBlockAct{});
     for (int l = 0; l < k.depth; ++l) {
       DitBlockAct& a = m.blk[l];
       a.x = f(M * D); a.rstd_a = f(M); a.h_a = h(M * D); a.qkv = h(M * Q); a.qkvb = h(M * Q);
       a.rq = f(M * Hh); a.rk = f(M * Hh); a.oa = h(M * D); a.lse_a = f(B * Hh * S); a.yo = f(M * D);
       a.x1 = f(M * D); a.rstd_c = f(M); a.hc = h(M * D); a.qf = f(M * Dq); a.cq = h(M * Dq); a.rcq = f(M * Hh);
-      a.kvf = f(MC * Dk); a.kvb = h(MC * Dk); a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
+      if (m.kv_batched) {
+        a.kvf = m.kvf_all ? m.kvf_all + l * Dk : nullptr;
+        a.kvb = m.kvb_all ? m.kvb_all + l * Dk : nullptr;
+      } else {
+        a.kvf = f(MC * Dk); a.kvb = h(MC * Dk);
+      }
+      a.kv_ld = kv_ld;
+      a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
       if (diff) {
         a.o1 = h(M * D); a.o2 = h(M * D); a.oc1 = h(M * D); a.oc2 = h(M * D);
         a.lse_a2 = f(B * Hh * S); a.lse_c2 = f(B * Hh * S); a.rq2 = f(M * Hh); a.rk2 = f(M * Hh); a.rcq2 = f(M * Hh);
@@ -582,11 +603,61 @@ static AttnArgs cross_attn(const DitBlockAct& a, int B, int H, int S, int C, int
   AttnArgs r;
   r.B = B; r.H = H; r.Sq = S; r.Sk = C; r.scale = scale; r.window = -1;
   r.q = a.cq + st * D; r.q_sb = (long)S * Dq; r.q_sh = 64; r.q_ld = Dq;
-  r.k = a.kvb + st * D; r.k_sb = (long)C * Dk; r.k_sh = 64; r.k_ld = Dk;
-  r.v = a.kvb + (Dk - D); r.v_sb = r.k_sb; r.v_sh = 64; r.v_ld = Dk;
+  r.k = a.kvb + st * D; r.k_sb = (long)C * a.kv_ld; r.k_sh = 64; r.k_ld = a.kv_ld;
+  r.v = a.kvb + (Dk - D); r.v_sb = r.k_sb; r.v_sh = 64; r.v_ld = a.kv_ld;
   r.o = o; r.o_sb = (long)S * D; r.o_sh = 64; r.o_ld = D;
   r.lse = st ? a.lse_c2 : a.lse_c;
   return r;
+}
+
+// The context K / V projections of all blocks (m.kv_batched): one GEMM over the stacked f16
+// weights when every block's cross.kv has its f16 operand copy in use, else one GEMM per block;
+// either way into kvf_all, block l at column l Dk.  The stacked copy is refilled when the model
+// generation changed (set_tensor); a refill recorded into a caller's graph repeats on every
+// replay, so it is only marked current when made outside a capture.
+static int context_kv_all(DitModel& m, int64_t MC, int64_t Dk, std::string& err) {
+  Ctx* c = m.c;
+  const int L = m.cfg.depth;
+  const int64_t ld = (int64_t)L * Dk;
+  std::vector<const Weight*> w(L);
+  bool stacked = true;
+  for (int l = 0; l < L; ++l) {
+    if (!(w[l] = m.weight(m.bname(l, "cross.kv.weight"), err))) return 1;
+    if (w[l]->out != Dk || w[l]->in != w[0]->in) { err = "cross.kv weights of different shapes"; return 1; }
+    stacked = stacked && w[l]->f16 &&
+              (w[l]->type == kTypeF16 || w[l]->type == kTypeF32 || !c->smem_dequant);
+  }
+  const int64_t K = w[0]->in;
+  if (!stacked) {
+    for (int l = 0; l < L; ++l) {
+      GemmDesc g;
+      g.M = (int)MC; g.N = (int)Dk; g.K = (int)K;
+      g.a = m.context_b; g.lda = K;
+      g.bsrc = kB_WEIGHT_NT; g.w = w[l];
+      g.out = m.kvf_all + l * Dk; g.ldo = ld;
+      g.name = "linear.fwd";
+      if (gemm(c, g, err)) return 1;
+    }
+    return 0;
+  }
+  if (!m.kv_w_all && !(m.kv_w_all = static_cast<__half*>(dmalloc(m, sizeof(__half) * (size_t)(ld * K), err))))
+    return 1;
+  if (m.kvw_mgen != m.gen) {
+    for (int l = 0; l < L; ++l)
+      if (cudaMemcpyAsync(m.kv_w_all + l * Dk * K, w[l]->f16, sizeof(__half) * (size_t)(Dk * K),
+                          cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+        return check_launch("stacked cross.kv weights", err);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess) cudaGetLastError();
+    if (cs == cudaStreamCaptureStatusNone) m.kvw_mgen = m.gen;
+  }
+  GemmDesc g;   // kvf_all = context W_all^T
+  g.M = (int)MC; g.N = (int)ld; g.K = (int)K;
+  g.a = m.context_b; g.lda = K;
+  g.bsrc = kB_F16_KMAJOR; g.b = m.kv_w_all; g.ldb = K;
+  g.out = m.kvf_all; g.ldo = ld;
+  g.name = "linear.fwd";
+  return gemm(c, g, err);
 }
 
 // ------------------------------------------------------------------ forward + backward
@@ -661,6 +732,7 @@ static int dit_step(DitModel& m, std::string& err) {
     if (!ssg) return 1;
     if (k_modulation(c, ssg, m.gcond, B, D, m.blk[l].mod, err)) return 1;
   }
+  if (m.kv_batched && context_kv_all(m, MC, Dk, err)) return 1;
   for (int l = 0; l < k.depth; ++l) {
     DitBlockAct& a = m.blk[l];
     float* x_next = l + 1 < k.depth ? m.blk[l + 1].x : m.x_final;
@@ -737,14 +809,15 @@ static int dit_step(DitModel& m, std::string& err) {
       if (k_head_prep_fwd(c, a.qf, (int)M, Dq, H, hs, diff ? 2 : 1, S, k.qk_eps, k.rot, k.rope_base, a.cq, err))
         return 1;
     }
-    if (lin_fwd(m, wckv, tkv, nullptr, m.context_b, MC, a.kvf, nullptr, err)) return 1;
+    if (!m.kv_batched && lin_fwd(m, wckv, tkv, nullptr, m.context_b, MC, a.kvf, nullptr, err)) return 1;
     {
       // [ck (| ckd) | cv], ck / ckd with cross.k_norm
       HeadSlice hs[3];
       hs[0].col = 0; hs[0].gamma = g_ck; hs[0].rstd = a.rck;
       if (diff) { hs[1].col = D; hs[1].gamma = g_ck; hs[1].rstd = a.rck2; }
       hs[diff ? 2 : 1].col = Dk - D;
-      if (k_head_prep_fwd(c, a.kvf, (int)MC, Dk, H, hs, diff ? 3 : 2, C, k.qk_eps, k.rot, k.rope_base, a.kvb, err))
+      if (k_head_prep_fwd(c, a.kvf, (int)MC, (int)a.kv_ld, H, hs, diff ? 3 : 2, C, k.qk_eps, k.rot, k.rope_base,
+                          a.kvb, err))
         return 1;
     }
     AttnArgs ca = cross_attn(a, B, H, S, C, D, Dq, Dk, scale, 0, diff ? a.oc1 : a.oc);
