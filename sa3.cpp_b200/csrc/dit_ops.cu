@@ -707,6 +707,22 @@ __global__ void copy_rows_kernel(const float* __restrict__ src, int src_rows_per
   }
 }
 
+// The same copy with 16-byte rows (D % 4 == 0, 16-byte aligned pointers): one block row per
+// copied row (grid-stride over rows), thread = 4 columns, no index division per element.
+__global__ void copy_rows4_kernel(const float* __restrict__ src, int src_rows_per, int src_off, float* __restrict__ dst,
+                                  __half* __restrict__ dst_h, int dst_rows_per, int dst_off, int B, int rows, int D) {
+  pdl_prologue();
+  const int c = 4 * (blockIdx.x * blockDim.x + threadIdx.x);
+  if (c >= D) return;
+  for (int rr = blockIdx.y; rr < B * rows; rr += gridDim.y) {
+    const int b = rr / rows, r = rr - b * rows;
+    const float4 v = *reinterpret_cast<const float4*>(src + ((long)b * src_rows_per + src_off + r) * D + c);
+    const long o = ((long)b * dst_rows_per + dst_off + r) * D + c;
+    if (dst) *reinterpret_cast<float4*>(dst + o) = v;
+    if (dst_h) *reinterpret_cast<uint2*>(dst_h + o) = make_uint2(pack_f16x2(v.x, v.y), pack_f16x2(v.z, v.w));
+  }
+}
+
 unsigned gs(long n, int threads = 256) {
   long b = (n + threads - 1) / threads;
   if (b > 148 * 16) b = 148 * 16;
@@ -944,6 +960,15 @@ int k_scale(Ctx* c, float* x, long n, float s, std::string& err) {
 int k_copy_rows(Ctx* c, const float* src, int src_rows_per, int src_off, float* dst, __half* dst_h,
                 int dst_rows_per, int dst_off, int B, int rows, int D, std::string& err) {
   ProfScope prof_(c, "copy_rows");
+  const auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (D % 4 == 0 && al16(src) && (!dst || al16(dst)) && (!dst_h || (reinterpret_cast<uintptr_t>(dst_h) & 7) == 0) &&
+      B > 0 && rows > 0) {
+    const long nrows = (long)B * rows;
+    const dim3 grid((unsigned)((D / 4 + 255) / 256), (unsigned)(nrows < 65535 ? nrows : 65535));
+    launch_pdl(c, copy_rows4_kernel, grid, 256, 0, src, src_rows_per, src_off, dst, dst_h, dst_rows_per, dst_off, B,
+               rows, D);
+    return check_launch("copy_rows", err);
+  }
   launch_pdl(c, copy_rows_kernel, gs((long)B * rows * D), 256, 0, src, src_rows_per, src_off, dst, dst_h, dst_rows_per,
                                                                   dst_off, B, rows, D);
   return check_launch("copy_rows", err);
