@@ -111,7 +111,8 @@ int k_mod_grad_norm(Ctx* c, const float* dh, const float* x, const float* rstd, 
                     int tps, long out_stride, float* dsc, float* dsh, std::string& err);
 int k_mod_grad_gate(Ctx* c, const float* gy, const float* y, const float* gate, long gate_stride, int T, int D, int tps,
                     long out_stride, float* dgate, std::string& err);
-int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err);
+// L blocks at once: ssg [L][6D], mod [L][B][6D]
+int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err, int L = 1);
 
 // loss[b] = sum((vel - target)^2) / (io*T) per sample; dvel = grad_scale * 2 (vel - target) / (io*T);
 // with weight (nullable, [B][io*T]): loss[b] = sum(w (vel - target)^2), dvel = grad_scale * 2 w (vel - target)

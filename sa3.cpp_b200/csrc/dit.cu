@@ -167,6 +167,11 @@ struct DitModel {
   // [MC][depth x Dk], block l at column l Dk
   bool kv_batched = false;
   __half* kv_w_all = nullptr;
+  // every block's ssg vector stacked [depth][6 dim] (refilled with the stacked K / V weights), so
+  // one launch forms all blocks' adaLN vectors into mod_all [depth][B][6 dim]
+  float* ssg_all = nullptr;
+  uint64_t ssg_mgen = ~0ull;
+  float* mod_all = nullptr;
   uint64_t kvw_mgen = ~0ull;
   float* kvf_all = nullptr;
   __half* kvb_all = nullptr;
@@ -376,6 +381,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     auto f = [&](int64_t n) { return static_cast<float*>(take(n * 4)); };
     auto h = [&](int64_t n) { return static_cast<__half*>(take(n * 2)); };
     m.kvf_all = m.kv_batched ? f(MC * kv_ld) : nullptr;
+    m.mod_all = f((int64_t)k.depth * B * 6 * D);
     m.kvb_all = m.kv_batched ? h(MC * kv_ld) : nullptr;
     m.blk.assign(k.depth, DitBlockAct{});
     for (int l = 0; l < k.depth; ++l) {
@@ -397,7 +403,7 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
         a.rck2 = f(MC * Hh);
       }
       a.x2 = f(M * D); a.rstd_f = f(M); a.hf = h(M * D); a.ff = h(M * 2 * I); a.act = h(M * I); a.yf = f(M * D);
-      a.mod = f(B * 6 * D);
+      a.mod = m.mod_all ? m.mod_all + (int64_t)l * B * 6 * D : nullptr;
       a.yc = m.tix.count(m.bname(l, "cross.out.weight")) ? f(M * D) : nullptr;
     }
     m.x_final = f(M * D);
@@ -727,10 +733,21 @@ static int dit_step(DitModel& m, std::string& err) {
   // ---------------- blocks (src/dit.h:164-266)
   // every block's adaLN vectors first: the residual kernel ending block l also forms the
   // modulated pre-norm input of block l + 1
-  for (int l = 0; l < k.depth; ++l) {
-    const float* ssg = m.vec(m.bname(l, "ssg"), err);
-    if (!ssg) return 1;
-    if (k_modulation(c, ssg, m.gcond, B, D, m.blk[l].mod, err)) return 1;
+  {
+    const size_t per = sizeof(float) * 6 * (size_t)D;
+    if (!m.ssg_all && !(m.ssg_all = static_cast<float*>(dmalloc(m, per * k.depth, err)))) return 1;
+    if (m.ssg_mgen != m.gen) {
+      for (int l = 0; l < k.depth; ++l) {
+        const float* ssg = m.vec(m.bname(l, "ssg"), err);
+        if (!ssg) return 1;
+        if (cudaMemcpyAsync(m.ssg_all + (size_t)l * 6 * D, ssg, per, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
+          return check_launch("stacked ssg", err);
+      }
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess) cudaGetLastError();
+      if (cs == cudaStreamCaptureStatusNone) m.ssg_mgen = m.gen;   // (a captured refill repeats per replay)
+    }
+    if (k_modulation(c, m.ssg_all, m.gcond, B, D, m.mod_all, err, k.depth)) return 1;
   }
   if (m.kv_batched && context_kv_all(m, MC, Dk, err)) return 1;
   for (int l = 0; l < k.depth; ++l) {

@@ -612,13 +612,15 @@ __global__ void __launch_bounds__(128) mod_colsum_kernel(const float* __restrict
   }
 }
 
-__global__ void modulation_kernel(const float* __restrict__ ssg, const float* __restrict__ gcond, int B, int D,
+// mod[l][b][j] = ssg[l][j] + gcond[b][j] for L blocks (ssg, mod with block strides 6D, B 6D);
+// slots 2 and 5 (the gates) leave as sigmoid(1 - v)
+__global__ void modulation_kernel(const float* __restrict__ ssg, const float* __restrict__ gcond, int L, int B, int D,
                                   float* __restrict__ mod) {
   pdl_prologue();
-  const long n = (long)B * 6 * D;
+  const long per = 6L * D, n = (long)L * B * per;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
-    const long j = i % (6L * D);
-    float v = ssg[j] + gcond[i];
+    const long l = i / ((long)B * per), bi = i - l * B * per, j = bi % per;
+    float v = ssg[l * per + j] + gcond[bi];
     const int slot = (int)(j / D);
     if (slot == 2 || slot == 5) v = 1.f / (__expf(v - 1.f) + 1.f);   // h * sigmoid(1 - g)
     mod[i] = v;
@@ -918,9 +920,9 @@ int k_mod_grad_gate(Ctx* c, const float* gy, const float* y, const float* gate, 
   return mod_colsum(c, gy, nullptr, nullptr, nullptr, y, gate, gate_stride, T, D, tps, out_stride, dgate, nullptr, err);
 }
 
-int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err) {
+int k_modulation(Ctx* c, const float* ssg, const float* gcond, int B, int D, float* mod, std::string& err, int L) {
   ProfScope prof_(c, "modulation");
-  launch_pdl(c, modulation_kernel, gs((long)B * 6 * D), 256, 0, ssg, gcond, B, D, mod);
+  launch_pdl(c, modulation_kernel, gs((long)L * B * 6 * D), 256, 0, ssg, gcond, L, B, D, mod);
   return check_launch("modulation", err);
 }
 
