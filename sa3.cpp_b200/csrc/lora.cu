@@ -314,17 +314,24 @@ __global__ void prep_all_kernel(const PrepDesc* __restrict__ descs) {
   const int stride = gridDim.x * blockDim.x;
   const int t0 = blockIdx.x * blockDim.x + threadIdx.x;
   const int nin = (int)d.in * 64, nout = (int)d.out * 64;
+  // each output walked in its own row-major order, so every store is coalesced: at_x [in][64] and
+  // b_x [out][64] along the padded rank (the A reads of at_x stride through A, which stays in
+  // cache), a_h [16][in] and bt_h [16][out] along in / out
   for (int k = t0; k < nin; k += stride) {
     const int i = k >> 6, c = k & 63;
-    const float a = (c < d.rank) ? d.A[(int64_t)c * d.in + i] : 0.f;
-    d.at_x[k] = __float2half_rn(a);
-    if (c < R) d.a_h[(int64_t)c * d.in + i] = __float2half_rn(a);
+    d.at_x[k] = __float2half_rn((c < d.rank) ? d.A[(int64_t)c * d.in + i] : 0.f);
+  }
+  for (int k = t0; k < R * (int)d.in; k += stride) {
+    const int c = k / (int)d.in;
+    d.a_h[k] = __float2half_rn((c < d.rank) ? d.A[k] : 0.f);
   }
   for (int k = t0; k < nout; k += stride) {
     const int o = k >> 6, c = k & 63;
-    const float b = (c < d.rank) ? d.B[(int64_t)o * d.rank + c] : 0.f;
-    d.b_x[k] = __float2half_rn(d.s * b);
-    if (c < R) d.bt_h[(int64_t)c * d.out + o] = __float2half_rn(b);
+    d.b_x[k] = __float2half_rn((c < d.rank) ? d.s * d.B[(int64_t)o * d.rank + c] : 0.f);
+  }
+  for (int k = t0; k < R * (int)d.out; k += stride) {
+    const int c = k / (int)d.out, o = k - c * (int)d.out;
+    d.bt_h[k] = __float2half_rn((c < d.rank) ? d.B[(int64_t)o * d.rank + c] : 0.f);
   }
 }
 
