@@ -61,6 +61,11 @@ struct HeadSlice {
 const float2* k_rope_table(Ctx* c, int tps, int rot, float rope_base, std::string& err);
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
                     int tokens_per_sample, float eps, int rot, float rope_base, __half* out, std::string& err);
+// the same slices `reps` times, repetition r at r col_step columns, its gamma r gamma_step values
+// on and its rstd r rstd_step entries on (one launch for every block's context K / V)
+int k_head_prep_fwd_reps(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                         int tokens_per_sample, float eps, int rot, float rope_base, __half* out, int reps,
+                         int col_step, int gamma_step, long rstd_step, std::string& err);
 // the same with f16 projection rows
 int k_head_prep_fwd(Ctx* c, const __half* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
                     int tokens_per_sample, float eps, int rot, float rope_base, __half* out, std::string& err);

@@ -172,6 +172,12 @@ struct DitModel {
   float* ssg_all = nullptr;
   uint64_t ssg_mgen = ~0ull;
   float* mod_all = nullptr;
+  // with the batched context K / V and no differential streams, their head preparation is one
+  // launch too: the blocks' cross.k_norm gammas stacked [depth][64] (refilled with ssg_all), the
+  // blocks' rstd of the context keys contiguous in rck_all [depth][MC][H]
+  bool kvp_batched = false;
+  float* gck_all = nullptr;
+  float* rck_all = nullptr;
   uint64_t kvw_mgen = ~0ull;
   float* kvf_all = nullptr;
   __half* kvb_all = nullptr;
@@ -382,6 +388,8 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
     auto h = [&](int64_t n) { return static_cast<__half*>(take(n * 2)); };
     m.kvf_all = m.kv_batched ? f(MC * kv_ld) : nullptr;
     m.mod_all = f((int64_t)k.depth * B * 6 * D);
+    m.kvp_batched = m.kv_batched && !diff;
+    m.rck_all = m.kvp_batched ? f((int64_t)k.depth * MC * Hh) : nullptr;
     m.kvb_all = m.kv_batched ? h(MC * kv_ld) : nullptr;
     m.blk.assign(k.depth, DitBlockAct{});
     for (int l = 0; l < k.depth; ++l) {
@@ -396,7 +404,9 @@ static int alloc_acts(DitModel& m, int B, int T, int C, std::string& err) {
         a.kvf = f(MC * Dk); a.kvb = h(MC * Dk);
       }
       a.kv_ld = kv_ld;
-      a.rck = f(MC * Hh); a.oc = h(M * D); a.lse_c = f(B * Hh * S);
+      if (m.kvp_batched) a.rck = m.rck_all ? m.rck_all + (int64_t)l * MC * Hh : nullptr;
+      else a.rck = f(MC * Hh);
+      a.oc = h(M * D); a.lse_c = f(B * Hh * S);
       if (diff) {
         a.o1 = h(M * D); a.o2 = h(M * D); a.oc1 = h(M * D); a.oc2 = h(M * D);
         a.lse_a2 = f(B * Hh * S); a.lse_c2 = f(B * Hh * S); a.rq2 = f(M * Hh); a.rk2 = f(M * Hh); a.rcq2 = f(M * Hh);
@@ -736,12 +746,21 @@ static int dit_step(DitModel& m, std::string& err) {
   {
     const size_t per = sizeof(float) * 6 * (size_t)D;
     if (!m.ssg_all && !(m.ssg_all = static_cast<float*>(dmalloc(m, per * k.depth, err)))) return 1;
+    if (m.kvp_batched && !m.gck_all && !(m.gck_all = static_cast<float*>(dmalloc(m, sizeof(float) * 64 * k.depth, err))))
+      return 1;
     if (m.ssg_mgen != m.gen) {
       for (int l = 0; l < k.depth; ++l) {
         const float* ssg = m.vec(m.bname(l, "ssg"), err);
         if (!ssg) return 1;
         if (cudaMemcpyAsync(m.ssg_all + (size_t)l * 6 * D, ssg, per, cudaMemcpyDeviceToDevice, c->stream) != cudaSuccess)
           return check_launch("stacked ssg", err);
+        if (m.kvp_batched) {
+          const float* gck = m.vec(m.bname(l, "cross.k_norm.gamma"), err);
+          if (!gck) return 1;
+          if (cudaMemcpyAsync(m.gck_all + (size_t)l * 64, gck, sizeof(float) * 64, cudaMemcpyDeviceToDevice,
+                              c->stream) != cudaSuccess)
+            return check_launch("stacked k_norm gammas", err);
+        }
       }
       cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
       if (cudaStreamIsCapturing(c->stream, &cs) != cudaSuccess) cudaGetLastError();
@@ -750,6 +769,15 @@ static int dit_step(DitModel& m, std::string& err) {
     if (k_modulation(c, m.ssg_all, m.gcond, B, D, m.mod_all, err, k.depth)) return 1;
   }
   if (m.kv_batched && context_kv_all(m, MC, Dk, err)) return 1;
+  if (m.kvp_batched) {
+    // [ck | cv] of every block: ck with its block's cross.k_norm, cv copied
+    HeadSlice hs[2];
+    hs[0].col = 0; hs[0].gamma = m.gck_all; hs[0].rstd = m.rck_all;
+    hs[1].col = Dk - D;
+    if (k_head_prep_fwd_reps(c, m.kvf_all, (int)MC, (int)((int64_t)k.depth * Dk), H, hs, 2, C, k.qk_eps, k.rot,
+                             k.rope_base, m.kvb_all, k.depth, (int)Dk, 64, (long)MC * H, err))
+      return 1;
+  }
   for (int l = 0; l < k.depth; ++l) {
     DitBlockAct& a = m.blk[l];
     float* x_next = l + 1 < k.depth ? m.blk[l + 1].x : m.x_final;
@@ -827,7 +855,7 @@ static int dit_step(DitModel& m, std::string& err) {
         return 1;
     }
     if (!m.kv_batched && lin_fwd(m, wckv, tkv, nullptr, m.context_b, MC, a.kvf, nullptr, err)) return 1;
-    {
+    if (!m.kvp_batched) {
       // [ck (| ckd) | cv], ck / ckd with cross.k_norm
       HeadSlice hs[3];
       hs[0].col = 0; hs[0].gamma = g_ck; hs[0].rstd = a.rck;

@@ -40,6 +40,10 @@ __global__ void rope_table_kernel(int tps, int rot, float log2_base, float2* __r
 struct HeadSlices {
   HeadSlice s[5];
   int n;
+  // the slices repeated `reps` times, repetition r shifted by r col_step columns, r gamma_step
+  // gamma values and r rstd_step rstd entries (the context K / V of every block in one launch)
+  int reps = 1, col_step = 0, gamma_step = 0;
+  long rstd_step = 0;
 };
 constexpr int kHpRows = 16;
 constexpr int kQkvRows = 32;   // qkv_bwd_dz: more rows per block, fewer dg atomics
@@ -256,9 +260,13 @@ __global__ void __launch_bounds__(256) head_prep_fwd_kernel(const Y* __restrict_
   pdl_prologue();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, j = lane & 7, q = lane >> 3;
   const int pair = blockIdx.x * 8 + warp;
-  if (pair >= H * slices.n) return;
-  const int si = pair / H, h = pair % H;
-  const HeadSlice sl = slices.s[si];
+  if (pair >= H * slices.n * slices.reps) return;
+  const int rp = pair / (H * slices.n), pr = pair - rp * H * slices.n;
+  const int si = pr / H, h = pr % H;
+  HeadSlice sl = slices.s[si];
+  sl.col += rp * slices.col_step;
+  if (sl.gamma) sl.gamma += rp * slices.gamma_step;
+  if (sl.rstd) sl.rstd += rp * slices.rstd_step;
   const int col = sl.col + h * 64 + 8 * j;
   float gm[8];
   if (sl.gamma) ld8(sl.gamma + 8 * j, gm);
@@ -794,10 +802,13 @@ const float2* k_rope_table(Ctx* c, int tps, int rot, float rope_base, std::strin
 
 template <typename Y>
 static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
-                           float eps, int rot, float rope_base, __half* out, std::string& err) {
+                           float eps, int rot, float rope_base, __half* out, std::string& err, int reps = 1,
+                           int col_step = 0, int gamma_step = 0, long rstd_step = 0) {
   if (rot != 0 && rot != 32 && rot != 64) { err = "rope: rot must be 32 or 64"; return 1; }
   if (nslices < 1 || nslices > 5) { err = "head_prep: 1..5 slices"; return 1; }
+  if (reps < 1) { err = "head_prep: reps must be positive"; return 1; }
   HeadSlices hs{};
+  hs.reps = reps; hs.col_step = col_step; hs.gamma_step = gamma_step; hs.rstd_step = rstd_step;
   bool any_rope = false;
   for (int i = 0; i < nslices; ++i) {
     hs.s[i] = slices[i];
@@ -808,7 +819,7 @@ static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const He
   if (any_rope && rot && !(tab = k_rope_table(c, tps, rot, rope_base, err))) return 1;
   ProfScope prof_(c, "head_prep_fwd");
   if ((T + kHpRows - 1) / kHpRows > 65535) { err = "head prep: too many rows"; return 1; }
-  const dim3 grid((unsigned)((H * nslices + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
+  const dim3 grid((unsigned)((H * nslices * reps + 7) / 8), (unsigned)((T + kHpRows - 1) / kHpRows));
   launch_pdl(c, head_prep_fwd_kernel<Y>, grid, 256, 0, y, T, ncols, H, hs, tps, eps, rot, tab, out);
   return check_launch("head_prep_fwd", err);
 }
@@ -816,6 +827,13 @@ static int head_prep_fwd_t(Ctx* c, const Y* y, int T, int ncols, int H, const He
 int k_head_prep_fwd(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices, int tps,
                     float eps, int rot, float rope_base, __half* out, std::string& err) {
   return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err);
+}
+
+int k_head_prep_fwd_reps(Ctx* c, const float* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
+                         int tps, float eps, int rot, float rope_base, __half* out, int reps, int col_step,
+                         int gamma_step, long rstd_step, std::string& err) {
+  return head_prep_fwd_t(c, y, T, ncols, H, slices, nslices, tps, eps, rot, rope_base, out, err, reps, col_step,
+                         gamma_step, rstd_step);
 }
 
 int k_head_prep_fwd(Ctx* c, const __half* y, int T, int ncols, int H, const HeadSlice* slices, int nslices,
