@@ -323,30 +323,40 @@ __global__ void __launch_bounds__(256) head_prep_bwd_kernel(const float* g, long
   if (sl.gamma) ld8(sl.gamma + 8 * j, gm);
   const int tb0 = blockIdx.y * kHpRows;
   int pos = (tb0 + q) % tps;
-#pragma unroll 2
-  for (int it = 0; it < kHpRows / 4 && tb0 + 4 * it < T; ++it) {
+  // every row set's loads first (gradient, the second stream's, the projection output, rstd),
+  // then the arithmetic and stores row set by row set
+  constexpr int NS = kHpRows / 4;
+  float ga[NS][8], ya[NS][8], ra[NS];
+#pragma unroll
+  for (int it = 0; it < NS; ++it) {
     const int t = tb0 + 4 * it + q;
-    const bool valid = t < T;
-    float gv[8], yv[8];
-    float r = 0.f;
-    if (valid) {
-      ld8(g + (long)t * g_ld + h * 64 + 8 * j, gv);
-      if (g2) {
-        float w[8];
-        ld8(g2 + (long)t * g2_ld + h * 64 + 8 * j, w);
-#pragma unroll
-        for (int k = 0; k < 8; ++k) gv[k] -= w[k];
-      }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] *= gscale;
+    ra[it] = 0.f;
+    if (t < T) {
+      ld8(g + (long)t * g_ld + h * 64 + 8 * j, ga[it]);
       if (sl.gamma) {
-        ld8(y + (long)t * ncols + sl.col + h * 64 + 8 * j, yv);
-        r = sl.rstd[(long)t * H + h];
+        ld8(y + (long)t * ncols + sl.col + h * 64 + 8 * j, ya[it]);
+        ra[it] = sl.rstd[(long)t * H + h];
       }
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) gv[k] = yv[k] = 0.f;
+      for (int k = 0; k < 8; ++k) ga[it][k] = ya[it][k] = 0.f;
     }
+  }
+#pragma unroll
+  for (int it = 0; it < NS; ++it) {
+    const int t = tb0 + 4 * it + q;
+    const bool valid = t < T;
+    float(&gv)[8] = ga[it];
+    float(&yv)[8] = ya[it];
+    const float r = ra[it];
+    if (valid && g2) {
+      float w[8];
+      ld8(g2 + (long)t * g2_ld + h * 64 + 8 * j, w);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) gv[k] -= w[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) gv[k] *= gscale;
     if (sl.rope && (rot == 32 || rot == 64)) rope8(gv, j, pos, rot, tab, true);
     if (sl.gamma) {
       float dot = 0.f;
