@@ -159,11 +159,6 @@ __global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __rest
     ld8(x_in + e, v);
     ld8(y + e, w);
     if (gate) ld8(gate + s * gstride + c, gv);
-    ld8(gamma + c, gm);
-    if (sc) {
-      ld8(sc + s * mod_stride + c, a);
-      ld8(sh + s * mod_stride + c, b);
-    }
 #pragma unroll
     for (int k = 0; k < 8; ++k) v[k] = gate ? fmaf(w[k], gv[k], v[k]) : v[k] + w[k];
     st8(x_out + e, v);
@@ -177,6 +172,13 @@ __global__ void __launch_bounds__(1024) residual_norm_kernel(const float* __rest
   const float r = rsqrtf(block_sum(ss, red) / (float)D + eps);
   if (threadIdx.x == 0 && rstd) rstd[row] = r;
   if (!act) return;
+  // the row-invariant vectors (gamma, the sample's scale / shift: cache-resident) only now, so
+  // they hold no registers while the row's own loads are in flight
+  ld8(gamma + c, gm);
+  if (sc) {
+    ld8(sc + s * mod_stride + c, a);
+    ld8(sh + s * mod_stride + c, b);
+  }
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     v[k] *= r * gm[k];
