@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(512) gate_bwd_dz_kernel(const float* __restric
 // first), with a grid of kSwiBlocks blocks per SM, so no partial last wave is left; dz = f16(g dy)
 // and, for DoRA, dg += colsum(dy (y - bias) / g) with the reciprocals of g taken once per thread.
 constexpr int kSwiRows = 4;
-constexpr int kSwiBlocks = 4;
+constexpr int kSwiBlocks = 3;
 
 __device__ __forceinline__ void f16x8(const uint4 w, float (&v)[8]) {
   const uint32_t u[4] = {w.x, w.y, w.z, w.w};
